@@ -1,0 +1,60 @@
+"""b200ds: a Blackwell-native (sm_100a) DeepSeek-V3-family inference engine.
+
+Typical use (one process per GPU under torchrun, or a single process)::
+
+    from b200ds import load_engine, SamplingParams
+    eng = load_engine("deepseek-v3-671b", weights="random")      # or a checkpoint dir
+    outs = eng.generate([[1, 2, 3]], SamplingParams(max_tokens=32))
+"""
+from __future__ import annotations
+
+from typing import Optional, Union
+
+import torch
+
+from .config import PRESETS, EngineConfig, ModelConfig
+from .engine.engine import Engine, GenerateOutput
+from .engine.request import SamplingParams
+
+__all__ = ["Engine", "EngineConfig", "ModelConfig", "SamplingParams", "GenerateOutput", "load_engine", "build_model_from"]
+
+
+def build_model_from(cfg: ModelConfig, ecfg: EngineConfig, weights: Union[str, dict] = "random",
+                     device=None, seed: int = 0, ps=None):
+    """Build this rank's DeepseekModel.  ``weights`` is "random" (random init
+    of the architecture), a checkpoint directory, or a full state dict."""
+    from .parallel.state import get_state
+    from .models import loader
+    from .models.reference import init_weights
+    ps = ps or get_state()
+    if device is None:
+        device = ps.device if ps.device.type == "cuda" else ("cuda" if torch.cuda.is_available() else "cpu")
+    if isinstance(weights, dict):
+        sd = weights
+    elif weights == "random":
+        from .models import random_init
+        if random_init.should_generate_on_device(cfg, device):
+            return random_init.build_random_model(cfg, ecfg, ps, device, seed)
+        sd = init_weights(cfg, seed=seed)
+    else:
+        sd = loader.load_checkpoint(weights)
+    return loader.build_model(cfg, ecfg, ps, sd, device=device)
+
+
+def load_engine(model: Union[str, ModelConfig] = "tiny", weights: Union[str, dict] = "random",
+                ecfg: Optional[EngineConfig] = None, device=None, seed: int = 0, **cfg_over) -> Engine:
+    """Create an Engine for a preset name / HF checkpoint dir / ModelConfig."""
+    import os
+    if isinstance(model, ModelConfig):
+        cfg = model
+    elif model in PRESETS:
+        cfg = PRESETS[model](**cfg_over)
+    elif os.path.isdir(model):
+        cfg = ModelConfig.from_hf(os.path.join(model, "config.json"))
+        if weights == "random":
+            weights = model
+    else:
+        raise ValueError(f"unknown model {model!r}")
+    ecfg = ecfg or EngineConfig()
+    m = build_model_from(cfg, ecfg, weights, device=device, seed=seed)
+    return Engine(m, ecfg)

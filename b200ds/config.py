@@ -1,0 +1,197 @@
+"""Model and engine configuration.
+
+`ModelConfig` carries the DeepSeek-V3 family architecture (MLA attention with
+q/kv low-rank projections and a decoupled RoPE key, dense first layers, then
+sigmoid-routed MoE with a shared expert) plus the V3.2-style sparse-attention
+indexer.  It reads a Hugging Face `config.json` (the fields DeepSeek-V3 ships)
+and offers the named presets the benchmarks use.
+
+Reference parity: the served model's facts are recovered in the reference from
+kernel constants (hq_unit.cu:36-37, route_e5.cu:4-12, fork_attn.py:174-237,
+levers.py:78-80); the reference takes its config from the absent SGLang fork.
+"""
+from __future__ import annotations
+
+import dataclasses
+import json
+import math
+from dataclasses import dataclass, field
+from typing import Optional
+
+
+@dataclass
+class ModelConfig:
+    vocab_size: int = 129280
+    hidden_size: int = 7168
+    intermediate_size: int = 18432          # dense-layer FFN width
+    moe_intermediate_size: int = 2048
+    num_hidden_layers: int = 61
+    first_k_dense_replace: int = 3
+    num_attention_heads: int = 128
+    q_lora_rank: Optional[int] = 1536
+    kv_lora_rank: int = 512
+    qk_nope_head_dim: int = 128
+    qk_rope_head_dim: int = 64
+    v_head_dim: int = 128
+    n_routed_experts: int = 256
+    n_shared_experts: int = 1
+    num_experts_per_tok: int = 8
+    n_group: int = 8
+    topk_group: int = 4
+    routed_scaling_factor: float = 2.5
+    scoring_func: str = "sigmoid"
+    norm_topk_prob: bool = True
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 10000.0
+    rope_scaling: Optional[dict] = field(default_factory=lambda: {
+        "type": "yarn", "factor": 40.0, "original_max_position_embeddings": 4096,
+        "beta_fast": 32.0, "beta_slow": 1.0, "mscale": 1.0, "mscale_all_dim": 1.0})
+    max_position_embeddings: int = 163840
+    tie_word_embeddings: bool = False
+    # Sparse attention (V3.2-style lightning indexer); 0 heads = dense MLA.
+    index_n_heads: int = 0
+    index_head_dim: int = 128
+    index_topk: int = 2048
+    # Weight formats: "mxfp8" (e4m3 + UE8M0 per 32 along K), "nvfp4"
+    # (e2m1 + e4m3 per 16 along K + fp32 global), "bf16" or "fp32".
+    dense_format: str = "mxfp8"
+    expert_format: str = "mxfp8"
+
+    # ---- derived -----------------------------------------------------------
+    @property
+    def qk_head_dim(self) -> int:
+        return self.qk_nope_head_dim + self.qk_rope_head_dim
+
+    @property
+    def kv_cache_dim(self) -> int:
+        """Latent (kv_lora_rank) + decoupled rope key per token."""
+        return self.kv_lora_rank + self.qk_rope_head_dim
+
+    def is_moe_layer(self, i: int) -> bool:
+        return self.n_routed_experts > 0 and i >= self.first_k_dense_replace
+
+    @property
+    def softmax_scale(self) -> float:
+        s = 1.0 / math.sqrt(self.qk_head_dim)
+        rs = self.rope_scaling
+        if rs and rs.get("type", rs.get("rope_type")) == "yarn":
+            m = yarn_mscale(rs["factor"], rs.get("mscale_all_dim", 0.0))
+            s = s * m * m
+        return s
+
+    def num_params(self) -> int:
+        h = self.hidden_size
+        H = self.num_attention_heads
+        qr = self.q_lora_rank or 0
+        attn = (h * qr + qr * H * self.qk_head_dim if qr else h * H * self.qk_head_dim)
+        attn += h * self.kv_cache_dim + self.kv_lora_rank * H * (self.qk_nope_head_dim + self.v_head_dim)
+        attn += H * self.v_head_dim * h
+        dense = 3 * h * self.intermediate_size
+        moe = (self.n_routed_experts + self.n_shared_experts) * 3 * h * self.moe_intermediate_size
+        moe += self.n_routed_experts * h
+        n_moe = sum(1 for i in range(self.num_hidden_layers) if self.is_moe_layer(i))
+        n_dense = self.num_hidden_layers - n_moe
+        emb = self.vocab_size * h * (1 if self.tie_word_embeddings else 2)
+        return self.num_hidden_layers * attn + n_dense * dense + n_moe * moe + emb
+
+    # ---- io ----------------------------------------------------------------
+    @classmethod
+    def from_hf(cls, path_or_dict) -> "ModelConfig":
+        """Build from a Hugging Face DeepSeek-V3 `config.json` (path or dict)."""
+        if isinstance(path_or_dict, dict):
+            d = path_or_dict
+        else:
+            with open(path_or_dict) as f:
+                d = json.load(f)
+        names = {f.name for f in dataclasses.fields(cls)}
+        kw = {k: v for k, v in d.items() if k in names}
+        if "index_n_heads" not in d and "index_head_dim" in d:
+            kw["index_n_heads"] = 64
+        qc = d.get("quantization_config") or {}
+        if qc.get("quant_method") == "fp8":
+            kw.setdefault("dense_format", "mxfp8")
+            kw.setdefault("expert_format", "mxfp8")
+        return cls(**kw)
+
+    def to_dict(self) -> dict:
+        return dataclasses.asdict(self)
+
+
+def yarn_mscale(scale: float, mscale: float = 1.0) -> float:
+    if scale <= 1.0:
+        return 1.0
+    return 0.1 * mscale * math.log(scale) + 1.0
+
+
+# ---------------------------------------------------------------------------
+# Presets
+# ---------------------------------------------------------------------------
+
+def tiny_config(**over) -> ModelConfig:
+    """2 layers (dense FFN 512, then MoE), hidden 256,
+    4 heads, q_lora 128, kv_lora 64, nope 32, rope 16, v 32, 8 experts top-2
+    sigmoid + 1 shared, moe_intermediate 128, vocab 1024."""
+    c = ModelConfig(
+        vocab_size=1024, hidden_size=256, intermediate_size=512, moe_intermediate_size=128,
+        num_hidden_layers=2, first_k_dense_replace=1, num_attention_heads=4,
+        q_lora_rank=128, kv_lora_rank=64, qk_nope_head_dim=32, qk_rope_head_dim=16,
+        v_head_dim=32, n_routed_experts=8, n_shared_experts=1, num_experts_per_tok=2,
+        n_group=1, topk_group=1, routed_scaling_factor=1.0, max_position_embeddings=4096,
+        rope_scaling=None, dense_format="fp32", expert_format="fp32")
+    return dataclasses.replace(c, **over)
+
+
+def v3_671b_config(**over) -> ModelConfig:
+    """DeepSeek-V3 shaped 671B decoder."""
+    return dataclasses.replace(ModelConfig(), **over)
+
+
+def v32_sparse_config(**over) -> ModelConfig:
+    """the 671B model with a 64-head fp8 lightning indexer
+    selecting top-2048 latent-KV tokens per query."""
+    return dataclasses.replace(ModelConfig(index_n_heads=64, index_head_dim=128, index_topk=2048), **over)
+
+
+def v3_nvfp4_config(**over) -> ModelConfig:
+    """routed experts in NVFP4, shared/dense in MXFP8."""
+    return dataclasses.replace(ModelConfig(expert_format="nvfp4", dense_format="mxfp8"), **over)
+
+
+def small_gpu_config(**over) -> ModelConfig:
+    """A V3-shaped model small enough for single-GPU unit tests (4 layers)."""
+    c = ModelConfig(
+        vocab_size=4096, hidden_size=1024, intermediate_size=2048, moe_intermediate_size=256,
+        num_hidden_layers=4, first_k_dense_replace=1, num_attention_heads=16,
+        q_lora_rank=384, kv_lora_rank=512, qk_nope_head_dim=128, qk_rope_head_dim=64,
+        v_head_dim=128, n_routed_experts=32, n_shared_experts=1, num_experts_per_tok=8,
+        n_group=4, topk_group=2, routed_scaling_factor=2.5, max_position_embeddings=8192)
+    return dataclasses.replace(c, **over)
+
+
+PRESETS = {
+    "tiny": tiny_config,
+    "deepseek-v3-671b": v3_671b_config,
+    "deepseek-v3.2-sparse-671b": v32_sparse_config,
+    "deepseek-v3-671b-nvfp4": v3_nvfp4_config,
+    "small": small_gpu_config,
+}
+
+
+@dataclass
+class EngineConfig:
+    """Serving-engine knobs (scheduler, KV pool, graphs, parallelism)."""
+    tp_size: int = 1                 # attention tensor parallel width
+    ep_size: int = 1                 # expert parallel width
+    dp_attention: bool = False       # data-parallel attention (tp_size=1 per DP rank) + EP MoE
+    page_size: int = 64              # tokens per KV page
+    max_num_seqs: int = 256          # concurrent running requests
+    max_prefill_tokens: int = 16384  # chunked-prefill budget per step
+    kv_cache_fraction: float = 0.85  # of free HBM after weights
+    max_kv_pages: Optional[int] = None
+    cuda_graphs: bool = True         # capture decode per batch bucket
+    graph_batch_sizes: tuple = (1, 2, 4, 8, 16, 32, 64, 128, 256)
+    enable_prefix_cache: bool = True
+    comm_impl: str = "fused"         # "fused" (own NVLink kernels) or "nccl" (baseline)
+    gemm_impl: str = "native"        # "native" (own tcgen05 kernels) or "torch" (baseline)
+    seed: int = 0
+    weight_sets: int = 0             # >0: cycle this many distinct layer weight sets (when the model exceeds HBM)

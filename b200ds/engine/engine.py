@@ -1,0 +1,170 @@
+"""`Engine`: the public serving API (`Engine.generate`), one instance per rank.
+
+Every rank of an SPMD job (torchrun, one process per GPU) constructs the
+Engine and calls `generate` with the same requests; schedules, page tables
+and sampled tokens are identical on every rank, so no host broadcast is
+needed between steps.  The server (b200ds.server) drives rank 0 and
+forwards requests to the other ranks over the gloo control group.
+
+Per step: the scheduler picks a prefill or decode batch; the host builds the
+flat batch metadata in pinned memory and copies it to the device; the model
+runs (decode steps replay a captured CUDA graph per padded batch size); the
+sampled token ids come back to the host.
+
+Reference parity: Engine.generate / the OpenAI server belong to SGLang
+(absent from the reference, which only replaces the forward:
+model_node.py:480-482 and the logits processor lgp.py:555).
+"""
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Sequence, Union
+
+import torch
+
+from .. import ops
+from ..config import EngineConfig, ModelConfig
+from ..kv.pool import PagePool
+from ..kv.radix import RadixCache
+from ..models.batch import ForwardBatch, build_batch
+from ..models.deepseek import DeepseekModel
+from ..parallel.state import ParallelState, get_state
+from .request import Request, SamplingParams
+from .scheduler import Scheduler, Step
+
+
+@dataclass
+class GenerateOutput:
+    rid: int
+    prompt_tokens: int
+    token_ids: List[int]
+    finish_reason: str
+    ttft_s: float
+    tpot_s: float
+    text: Optional[str] = None
+
+
+class Engine:
+    def __init__(self, model: DeepseekModel, ecfg: EngineConfig, num_pages: Optional[int] = None,
+                 eos_token_id: Optional[int] = None, tokenizer=None):
+        self.model = model
+        self.cfg: ModelConfig = model.cfg
+        self.ecfg = ecfg
+        self.ps: ParallelState = model.ps
+        self.device = model.device
+        if num_pages is None:
+            num_pages = ecfg.max_kv_pages or self._auto_pages()
+        self.pool = PagePool(num_pages, ecfg.page_size)
+        model.allocate_kv(num_pages)
+        self.radix = RadixCache(self.pool) if ecfg.enable_prefix_cache else None
+        self.sched = Scheduler(self.pool, ecfg.max_num_seqs, ecfg.max_prefill_tokens, self.radix)
+        self.eos = eos_token_id
+        self.tokenizer = tokenizer
+        self._next_rid = 0
+        self.graphs = None
+        if self.device.type == "cuda" and ecfg.cuda_graphs:
+            from .cuda_graph import DecodeGraphRunner
+            self.graphs = DecodeGraphRunner(self)
+        self.stats: Dict[str, float] = {"steps": 0, "prefill_tokens": 0, "decode_tokens": 0}
+
+    def _auto_pages(self) -> int:
+        if self.device.type != "cuda":
+            return 1024
+        free, _ = torch.cuda.mem_get_info(self.device)
+        per_page = self.model.kv_bytes_per_token() * self.ecfg.page_size
+        return max(16, int(free * self.ecfg.kv_cache_fraction) // per_page)
+
+    # ------------------------------------------------------------------
+    def add_request(self, prompt: Union[str, Sequence[int]], params: Optional[SamplingParams] = None) -> Request:
+        if isinstance(prompt, str):
+            assert self.tokenizer is not None, "text prompts need a tokenizer"
+            prompt = self.tokenizer.encode(prompt)
+        r = Request(self._next_rid, list(prompt), params or SamplingParams())
+        self._next_rid += 1
+        self.sched.add(r)
+        return r
+
+    def _forward(self, step: Step) -> List[int]:
+        seqs = [{"tokens": ch, "start": st, "pages": r.pages}
+                for r, ch, st in zip(step.reqs, step.chunks, step.starts)]
+        if step.kind == "decode" and self.graphs is not None and self.graphs.can_run(len(seqs)):
+            return self.graphs.run(step, seqs)
+        fb = build_batch(seqs, self.ecfg.page_size, device="cpu")
+        fb = self._to_device(fb)
+        logits = self.model.forward(fb)
+        return self._sample(step, logits)
+
+    def _to_device(self, fb: ForwardBatch) -> ForwardBatch:
+        if self.device.type == "cpu":
+            return fb
+        kw = {}
+        for k, v in fb.__dict__.items():
+            if isinstance(v, torch.Tensor):
+                kw[k] = v.pin_memory().to(self.device, non_blocking=True)
+            else:
+                kw[k] = v
+        return ForwardBatch(**kw)
+
+    def _sample(self, step: Step, logits: torch.Tensor) -> List[int]:
+        B = logits.shape[0]
+        temp = torch.tensor([r.params.temperature for r in step.reqs], dtype=torch.float32)
+        if bool((temp <= 0).all()):
+            return logits.argmax(-1).tolist()
+        top_p = torch.tensor([r.params.top_p for r in step.reqs], dtype=torch.float32)
+        top_k = torch.tensor([r.params.top_k for r in step.reqs], dtype=torch.int32)
+        u = torch.tensor([r.uniform() if s else 0.0 for r, s in zip(step.reqs, step.sample)],
+                         dtype=torch.float32)
+        dev = logits.device
+        return ops.sample(logits, temp.to(dev), top_p.to(dev), top_k.to(dev), u.to(dev)).tolist()
+
+    def step(self) -> List[Request]:
+        """Run one scheduler step; returns requests that finished."""
+        st = self.sched.next_step()
+        if st is None:
+            return []
+        toks = self._forward(st)
+        self.sched.commit(st)
+        now = time.perf_counter()
+        done = []
+        self.stats["steps"] += 1
+        if st.kind == "prefill":
+            self.stats["prefill_tokens"] += sum(len(c) for c in st.chunks)
+        else:
+            self.stats["decode_tokens"] += len(st.reqs)
+        for r, smp, t in zip(st.reqs, st.sample, toks):
+            if not smp:
+                continue
+            r.output.append(int(t))
+            r.token_times.append(now)
+            if r.t_first is None:
+                r.t_first = now
+            p = r.params
+            if len(r.output) >= p.max_tokens:
+                r.finished, r.finish_reason = True, "length"
+            elif not p.ignore_eos and ((self.eos is not None and t == self.eos) or t in p.stop_token_ids):
+                r.finished, r.finish_reason = True, "stop"
+            if r.finished:
+                r.t_done = now
+                self.sched.finish(r)
+                done.append(r)
+        return done
+
+    def generate(self, prompts: Sequence[Union[str, Sequence[int]]],
+                 params: Union[SamplingParams, Sequence[SamplingParams], None] = None) -> List[GenerateOutput]:
+        """Run the prompts to completion and return one output per prompt
+        (in order).  Identical calls on every rank of an SPMD job produce
+        identical results."""
+        if params is None or isinstance(params, SamplingParams):
+            params = [params or SamplingParams()] * len(prompts)
+        reqs = [self.add_request(p, sp) for p, sp in zip(prompts, params)]
+        while any(not r.finished for r in reqs):
+            self.step()
+        outs = []
+        for r in reqs:
+            n = len(r.output)
+            tpot = (r.t_done - r.t_first) / (n - 1) if n > 1 else 0.0
+            text = self.tokenizer.decode(r.output) if self.tokenizer is not None else None
+            outs.append(GenerateOutput(r.rid, len(r.prompt), list(r.output), r.finish_reason or "length",
+                                       (r.t_first or r.t_arrive) - r.t_arrive, tpot, text))
+        return outs

@@ -1,0 +1,51 @@
+"""Request and sampling-parameter records."""
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+from typing import List, Optional
+
+import torch
+
+
+@dataclass
+class SamplingParams:
+    max_tokens: int = 16
+    temperature: float = 0.0        # <= 0: greedy
+    top_p: float = 1.0
+    top_k: int = 0                  # <= 0: disabled
+    seed: Optional[int] = None
+    ignore_eos: bool = False
+    stop_token_ids: List[int] = field(default_factory=list)
+
+
+@dataclass
+class Request:
+    rid: int
+    prompt: List[int]
+    params: SamplingParams
+    output: List[int] = field(default_factory=list)
+    pages: List[int] = field(default_factory=list)
+    cached: int = 0                  # tokens whose KV is in the cache
+    prefix_nodes: list = field(default_factory=list)
+    prefix_pages: int = 0            # leading pages shared with the radix cache
+    finished: bool = False
+    finish_reason: Optional[str] = None
+    t_arrive: float = field(default_factory=time.perf_counter)
+    t_first: Optional[float] = None
+    t_done: Optional[float] = None
+    token_times: List[float] = field(default_factory=list)
+    gen: Optional[torch.Generator] = None
+
+    @property
+    def all_tokens(self) -> List[int]:
+        return self.prompt + self.output
+
+    @property
+    def total_len(self) -> int:
+        return len(self.prompt) + len(self.output)
+
+    def uniform(self) -> float:
+        if self.gen is None:
+            self.gen = torch.Generator().manual_seed(self.params.seed if self.params.seed is not None else self.rid)
+        return float(torch.rand((), generator=self.gen))

@@ -1,0 +1,209 @@
+"""Production DeepSeek-V3(.2) decoder for the serving engine.
+
+Layout per rank (one process per GPU):
+  * attention: TP over heads; q_a/kv_a projections fused into one replicated
+    GEMM; absorbed MLA over a paged e4m3 latent cache (kv_lora + rope per
+    token, one per-layer scale); o_proj row-parallel followed by the TP
+    all-reduce, fused with the residual add + next RMSNorm + MXFP8 quant;
+  * dense FFN: column/row parallel, SwiGLU + requant fused into the gate_up
+    GEMM epilogue, all-reduce fused as above;
+  * MoE: sigmoid group-limited router, routed experts expert-parallel (each
+    rank owns n_experts/ep contiguous experts), shared expert TP-split; one
+    fused combine + all-reduce + residual + norm + quant per layer;
+  * data-parallel attention (dp_attention): each rank runs attention for its
+    own requests with all heads; the MoE boundary all-gathers tokens and
+    reduce-scatters the combined result.
+
+Reference parity: fork_loop.py:229-400 (layer loop), fork_attn.py:75-553
+(attention), moe_fwd.py:67-263 (MoE), fin.py:384 (fused finalize +
+all-reduce + norm + quant), epa.py:1208 (o_proj GEMM + all-reduce).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Dict, List, Optional
+
+import torch
+
+from .. import ops
+from ..config import EngineConfig, ModelConfig
+from ..parallel.state import ParallelState
+from ..ops.quant import MXFP8Tensor
+from .batch import ForwardBatch
+from .rope import cos_sin_table
+
+
+class Linear:
+    """y = x W^T with W either a float tensor (tiny/CPU) or an MXFP8Tensor."""
+
+    def __init__(self, w):
+        self.w = w
+
+    @property
+    def quantized(self) -> bool:
+        return isinstance(self.w, MXFP8Tensor)
+
+    @property
+    def out_features(self) -> int:
+        return self.w.shape[0]
+
+    def __call__(self, x, out_dtype=torch.bfloat16) -> torch.Tensor:
+        return ops.linear(x, self.w, out_dtype)
+
+
+@dataclass
+class AttnWeights:
+    qkv_a: Linear                 # [q_lora + kv_lora + rope, h] (or q_proj-less variant)
+    q_a_ln: Optional[torch.Tensor]
+    kv_a_ln: torch.Tensor
+    q_b: Linear                   # [Hl * qk_head, q_lora]
+    w_uk: torch.Tensor            # [Hl, nope, kv_lora]
+    w_uv: torch.Tensor            # [Hl, v, kv_lora]
+    o_proj: Linear                # [h, Hl * v]
+    # sparse indexer (optional)
+    ix_wq_b: Optional[Linear] = None
+    ix_wk: Optional[torch.Tensor] = None
+    ix_k_norm_w: Optional[torch.Tensor] = None
+    ix_k_norm_b: Optional[torch.Tensor] = None
+    ix_weights: Optional[torch.Tensor] = None
+
+
+@dataclass
+class MoEWeights:
+    gate: torch.Tensor            # [E, h] fp32 router
+    bias: torch.Tensor            # [E]
+    experts: "ops.ExpertWeights"  # local experts, stacked
+    shared_gate_up: Optional[Linear]
+    shared_down: Optional[Linear]
+
+
+@dataclass
+class DenseWeights:
+    gate_up: Linear               # [2 * I_local, h] (gate rows then up rows)
+    down: Linear                  # [h, I_local]
+
+
+@dataclass
+class LayerWeights:
+    in_ln: torch.Tensor
+    post_ln: torch.Tensor
+    attn: AttnWeights
+    ffn: object                   # DenseWeights | MoEWeights
+
+
+class DeepseekModel:
+    def __init__(self, cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState,
+                 layers: List[LayerWeights], embed: torch.Tensor, final_ln: torch.Tensor,
+                 lm_head: torch.Tensor, device, kv_dtype=torch.float8_e4m3fn):
+        self.cfg, self.ecfg, self.ps = cfg, ecfg, ps
+        self.layers = layers
+        self.embed = embed
+        self.final_ln = final_ln
+        self.lm_head = lm_head            # [V_local, h] (vocab-parallel over TP)
+        self.device = torch.device(device)
+        self.kv_dtype = kv_dtype
+        attn_tp = 1 if ecfg.dp_attention else ps.tp_size
+        self.attn_tp = attn_tp
+        self.heads = cfg.num_attention_heads // attn_tp
+        self.rope_table = cos_sin_table(cfg, cfg.max_position_embeddings, device=self.device)
+        self.kv_scale = [1.0] * len(layers)
+        self.kv_cache: List[torch.Tensor] = []
+        self.ix_cache: List[torch.Tensor] = []
+        self.ix_scale: List[torch.Tensor] = []
+        self.page_size = ecfg.page_size
+
+    # ------------------------------------------------------------------
+    def allocate_kv(self, num_pages: int):
+        c = self.cfg
+        slots = num_pages * self.page_size
+        self.kv_cache = [torch.zeros(slots, c.kv_cache_dim, dtype=self.kv_dtype, device=self.device)
+                         for _ in self.layers]
+        if c.index_n_heads:
+            idt = self.kv_dtype
+            self.ix_cache = [torch.zeros(slots, c.index_head_dim, dtype=idt, device=self.device)
+                             for _ in self.layers]
+            self.ix_scale = [torch.ones(slots, dtype=torch.float32, device=self.device)
+                             for _ in self.layers]
+
+    def kv_bytes_per_token(self) -> int:
+        c = self.cfg
+        per = c.kv_cache_dim * torch.tensor([], dtype=self.kv_dtype).element_size()
+        if c.index_n_heads:
+            per += c.index_head_dim * torch.tensor([], dtype=self.kv_dtype).element_size() + 4
+        return per * len(self.layers)
+
+    # ------------------------------------------------------------------
+    def _attention(self, i: int, lw: LayerWeights, h, fb: ForwardBatch) -> torch.Tensor:
+        c = self.cfg
+        aw = lw.attn
+        T = fb.num_tokens
+        qkv = aw.qkv_a(h, out_dtype=torch.float32 if self.device.type == "cpu" else torch.bfloat16)
+        ql = c.q_lora_rank
+        q_lat = ops.rmsnorm(qkv[:, :ql], aw.q_a_ln, c.rms_norm_eps)
+        ops.kv_store(qkv[:, ql:], aw.kv_a_ln, c.rms_norm_eps, self.rope_table, fb.positions,
+                     self.kv_cache[i], fb.out_slots, self.kv_scale[i], c.kv_lora_rank)
+        q = aw.q_b(q_lat, out_dtype=torch.float32 if self.device.type == "cpu" else torch.bfloat16)
+        q = q.view(T, self.heads, c.qk_head_dim)
+        q_pe = ops.rope(q[..., c.qk_nope_head_dim:], fb.positions, self.rope_table)
+        q_abs = ops.absorb_q(q[..., : c.qk_nope_head_dim], aw.w_uk)       # [T, Hl, kv_lora]
+        topk = None
+        if c.index_n_heads:
+            topk = self._indexer(i, aw, h, q_lat, fb)
+        o_lat = ops.mla_attention(q_abs, q_pe, self.kv_cache[i], self.kv_scale[i], fb,
+                                  c.softmax_scale, self.page_size, topk)
+        o = ops.absorb_o(o_lat, aw.w_uv)                                  # [T, Hl*v]
+        return aw.o_proj(o, out_dtype=torch.float32 if self.device.type == "cpu" else torch.bfloat16)
+
+    def _indexer(self, i, aw: AttnWeights, h, q_lat, fb: ForwardBatch):
+        c = self.cfg
+        T = fb.num_tokens
+        nh, hd, rd = c.index_n_heads, c.index_head_dim, c.qk_rope_head_dim
+        xf = ops.to_float(h)
+        q = aw.ix_wq_b(q_lat, out_dtype=torch.float32).view(T, nh, hd)
+        q = torch.cat([ops.rope(q[..., :rd], fb.positions, self.rope_table), q[..., rd:].float()], -1)
+        k = torch.nn.functional.layer_norm(xf @ aw.ix_wk.float().T, (hd,), aw.ix_k_norm_w.float(),
+                                           aw.ix_k_norm_b.float(), 1e-6)
+        k = torch.cat([ops.rope(k[:, :rd], fb.positions, self.rope_table), k[:, rd:]], -1)
+        ops.index_k_store(k, self.ix_cache[i], self.ix_scale[i], fb.out_slots)
+        wts = (xf @ aw.ix_weights.float().T) * (nh ** -0.5) * (hd ** -0.5)
+        return ops.indexer_topk(q, wts, self.ix_cache[i], self.ix_scale[i], fb, self.page_size, c.index_topk)
+
+    def _ffn(self, i: int, lw: LayerWeights, h, fb: ForwardBatch) -> torch.Tensor:
+        c = self.cfg
+        out_dt = torch.float32 if self.device.type == "cpu" else torch.bfloat16
+        if isinstance(lw.ffn, DenseWeights):
+            a = ops.gate_up_swiglu(h, lw.ffn.gate_up)
+            return lw.ffn.down(a, out_dtype=out_dt)
+        mw: MoEWeights = lw.ffn
+        w, ids = ops.router(h, mw.gate, mw.bias, c)
+        out = ops.moe_experts(h, w, ids, mw.experts, out_dtype=out_dt)
+        if mw.shared_gate_up is not None:
+            s = lw.ffn.shared_down(ops.gate_up_swiglu(h, mw.shared_gate_up), out_dtype=out_dt)
+            out = out + s
+        return out
+
+    # ------------------------------------------------------------------
+    @torch.no_grad()
+    def forward(self, fb: ForwardBatch) -> torch.Tensor:
+        """Returns logits [B, V] (full vocab) for each sequence's last token."""
+        c = self.cfg
+        x = self.embed[fb.input_ids.long()].float() if self.device.type == "cpu" else self.embed[fb.input_ids.long()]
+        residual = x
+        h = ops.rmsnorm_act(residual, self.layers[0].in_ln, c.rms_norm_eps, self.layers[0].attn.qkv_a)
+        for i, lw in enumerate(self.layers):
+            a = self._attention(i, lw, h, fb)
+            h, residual = ops.allreduce_add_rmsnorm(a, residual, lw.post_ln, c.rms_norm_eps,
+                                                    self.ps, "tp_attn", self._ffn_first_linear(lw))
+            f = self._ffn(i, lw, h, fb)
+            nxt = self.layers[i + 1] if i + 1 < len(self.layers) else None
+            h, residual = ops.allreduce_add_rmsnorm(
+                f, residual, nxt.in_ln if nxt else self.final_ln, c.rms_norm_eps, self.ps,
+                "ffn", nxt.attn.qkv_a if nxt else None)
+        last = ops.to_float(h)[fb.last_idx] if not isinstance(h, torch.Tensor) or h.dim() == 2 else h[fb.last_idx]
+        return ops.lm_head_logits(last, self.lm_head, self.ps)
+
+    def _ffn_first_linear(self, lw: LayerWeights):
+        if isinstance(lw.ffn, DenseWeights):
+            return lw.ffn.gate_up
+        return lw.ffn.shared_gate_up

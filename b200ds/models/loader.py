@@ -1,0 +1,176 @@
+"""Weight construction: HF state dicts / safetensors checkpoints (fp8 with
+128x128 `weight_scale_inv` block scales) and random init generated directly
+in each rank's shard, in the serving formats.
+
+Reference parity: the reference serves weights loaded by SGLang (absent) and
+converts 32x32 ue8m0 block-FP8 to MXFP8 at bind time (dt.py:1-5, fl.py:1-10).
+"""
+from __future__ import annotations
+
+import glob
+import json
+import os
+from typing import Dict, Iterable, List, Optional
+
+import torch
+
+from ..config import EngineConfig, ModelConfig
+from ..ops import ExpertWeights
+from ..ops.quant import MXFP8Tensor, mxfp8_from_block128, quant_mxfp8_ref, pack_sf, sf_packed_size
+from ..parallel.state import ParallelState
+from .deepseek import AttnWeights, DeepseekModel, DenseWeights, LayerWeights, Linear, MoEWeights
+
+
+def _quantize(w: torch.Tensor, fmt: str, device) -> object:
+    """float weight [N, K] -> serving format on device."""
+    if fmt in ("fp32", "bf16"):
+        return w.to(device=device, dtype=torch.float32 if fmt == "fp32" else torch.bfloat16)
+    if fmt == "mxfp8":
+        wd = w.to(device)
+        if wd.is_cuda:
+            from .. import ops
+            a = ops.quant(wd.to(torch.bfloat16))
+            return MXFP8Tensor(a.q, a.sf)
+        q, sf = quant_mxfp8_ref(wd.float())
+        return MXFP8Tensor(q, sf)
+    raise ValueError(f"unknown weight format {fmt}")
+
+
+def _stack(ws: List[object]) -> object:
+    if isinstance(ws[0], MXFP8Tensor):
+        return MXFP8Tensor(torch.stack([w.data for w in ws]), torch.stack([w.sf for w in ws]))
+    return torch.stack(ws)
+
+
+def build_model(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState,
+                sd: Dict[str, torch.Tensor], device="cpu", kv_dtype=None) -> DeepseekModel:
+    """Build this rank's model from a FULL (unsharded) HF-named state dict of
+    float tensors (or fp8 + `<name>_scale_inv`)."""
+    dev = torch.device(device)
+    attn_tp = 1 if ecfg.dp_attention else ps.tp_size
+    attn_rank = 0 if ecfg.dp_attention else ps.tp_rank
+    tp, tr = ps.tp_size, ps.tp_rank
+    H = cfg.num_attention_heads
+    Hl = H // attn_tp
+
+    def get(name) -> torch.Tensor:
+        t = sd[name]
+        si = sd.get(name + "_scale_inv")
+        if si is not None:
+            N, K = t.shape
+            s = si.float().repeat_interleave(128, 0)[:N].repeat_interleave(128, 1)[:, :K]
+            t = t.float() * s
+        return t.float()
+
+    def split(t, dim, n, r):
+        return t.chunk(n, dim)[r].contiguous() if n > 1 else t
+
+    fmt_d = cfg.dense_format
+    layers: List[LayerWeights] = []
+    for i in range(cfg.num_hidden_layers):
+        p = f"model.layers.{i}."
+        a = p + "self_attn."
+        qa = get(a + "q_a_proj.weight")
+        kva = get(a + "kv_a_proj_with_mqa.weight")
+        qkv_a = Linear(_quantize(torch.cat([qa, kva], 0), fmt_d, dev))
+        qb = split(get(a + "q_b_proj.weight").view(H, cfg.qk_head_dim, -1), 0, attn_tp, attn_rank)
+        q_b = Linear(_quantize(qb.reshape(Hl * cfg.qk_head_dim, -1), fmt_d, dev))
+        kvb = split(get(a + "kv_b_proj.weight").view(H, cfg.qk_nope_head_dim + cfg.v_head_dim, -1), 0,
+                    attn_tp, attn_rank)
+        wdt = torch.bfloat16 if dev.type == "cuda" else torch.float32
+        w_uk = kvb[:, : cfg.qk_nope_head_dim].contiguous().to(dev, wdt)
+        w_uv = kvb[:, cfg.qk_nope_head_dim:].contiguous().to(dev, wdt)
+        o = split(get(a + "o_proj.weight"), 1, attn_tp, attn_rank)
+        aw = AttnWeights(qkv_a=qkv_a, q_a_ln=sd[a + "q_a_layernorm.weight"].float().to(dev),
+                         kv_a_ln=sd[a + "kv_a_layernorm.weight"].float().to(dev), q_b=q_b,
+                         w_uk=w_uk, w_uv=w_uv, o_proj=Linear(_quantize(o, fmt_d, dev)))
+        if cfg.index_n_heads:
+            ix = a + "indexer."
+            aw.ix_wq_b = Linear(get(ix + "wq_b.weight").to(dev, wdt))
+            aw.ix_wk = get(ix + "wk.weight").to(dev, wdt)
+            aw.ix_k_norm_w = sd[ix + "k_norm.weight"].float().to(dev)
+            aw.ix_k_norm_b = sd[ix + "k_norm.bias"].float().to(dev)
+            aw.ix_weights = get(ix + "weights_proj.weight").to(dev, wdt)
+        m = p + "mlp."
+        if cfg.is_moe_layer(i):
+            per = cfg.n_routed_experts // ps.ep_size
+            first = ps.ep_rank * per
+            w13, w2 = [], []
+            for e in range(first, first + per):
+                q = m + f"experts.{e}."
+                w13.append(_quantize(torch.cat([get(q + "gate_proj.weight"), get(q + "up_proj.weight")], 0),
+                                     cfg.expert_format, dev))
+                w2.append(_quantize(get(q + "down_proj.weight"), cfg.expert_format, dev))
+            ex = ExpertWeights(first=first, count=per, w13=_stack(w13), w2=_stack(w2),
+                               inter=cfg.moe_intermediate_size)
+            sgu = sdn = None
+            if cfg.n_shared_experts:
+                q = m + "shared_experts."
+                g = split(get(q + "gate_proj.weight"), 0, tp, tr)
+                u = split(get(q + "up_proj.weight"), 0, tp, tr)
+                sgu = Linear(_quantize(torch.cat([g, u], 0), fmt_d, dev))
+                sdn = Linear(_quantize(split(get(q + "down_proj.weight"), 1, tp, tr), fmt_d, dev))
+            ffn = MoEWeights(gate=get(m + "gate.weight").to(dev),
+                             bias=sd[m + "gate.e_score_correction_bias"].float().to(dev),
+                             experts=ex, shared_gate_up=sgu, shared_down=sdn)
+        else:
+            g = split(get(m + "gate_proj.weight"), 0, tp, tr)
+            u = split(get(m + "up_proj.weight"), 0, tp, tr)
+            ffn = DenseWeights(gate_up=Linear(_quantize(torch.cat([g, u], 0), fmt_d, dev)),
+                               down=Linear(_quantize(split(get(m + "down_proj.weight"), 1, tp, tr), fmt_d, dev)))
+        layers.append(LayerWeights(in_ln=sd[p + "input_layernorm.weight"].float().to(dev),
+                                   post_ln=sd[p + "post_attention_layernorm.weight"].float().to(dev),
+                                   attn=aw, ffn=ffn))
+    emb_dt = torch.bfloat16 if dev.type == "cuda" else torch.float32
+    embed = sd["model.embed_tokens.weight"].float().to(dev, emb_dt)
+    head_full = sd["model.embed_tokens.weight"] if cfg.tie_word_embeddings else sd["lm_head.weight"]
+    head = split(head_full.float(), 0, tp, tr).to(dev, emb_dt)
+    if kv_dtype is None:
+        kv_dtype = torch.float8_e4m3fn if dev.type == "cuda" else torch.float32
+    return DeepseekModel(cfg, ecfg, ps, layers, embed, sd["model.norm.weight"].float().to(dev), head, dev,
+                         kv_dtype=kv_dtype)
+
+
+# ---------------------------------------------------------------------------
+# safetensors checkpoints
+# ---------------------------------------------------------------------------
+
+def load_checkpoint(path: str, names: Optional[Iterable[str]] = None) -> Dict[str, torch.Tensor]:
+    """Read every tensor (or the listed ones) of a HF safetensors checkpoint
+    directory; fp8 tensors keep their `_scale_inv` companions."""
+    from safetensors import safe_open
+    out: Dict[str, torch.Tensor] = {}
+    want = set(names) if names is not None else None
+    files = sorted(glob.glob(os.path.join(path, "*.safetensors")))
+    for f in files:
+        with safe_open(f, framework="pt") as fh:
+            for k in fh.keys():
+                if want is None or k in want or k.replace("_scale_inv", "") in want:
+                    out[k] = fh.get_tensor(k)
+    return out
+
+
+def save_checkpoint_fp8(sd: Dict[str, torch.Tensor], path: str, cfg: ModelConfig, shard_bytes: int = 1 << 30):
+    """Write a state dict as a DeepSeek-style fp8 checkpoint: every 2-D
+    projection weight as e4m3 + fp32 128x128 `weight_scale_inv`."""
+    from safetensors.torch import save_file
+    os.makedirs(path, exist_ok=True)
+    out: Dict[str, torch.Tensor] = {}
+    for k, v in sd.items():
+        if v.dim() == 2 and k.endswith("proj.weight") or (".experts." in k and v.dim() == 2):
+            N, K = v.shape
+            nb, kb = (N + 127) // 128, (K + 127) // 128
+            pad = torch.zeros(nb * 128, kb * 128)
+            pad[:N, :K] = v.float()
+            blk = pad.view(nb, 128, kb, 128).abs().amax((1, 3)).clamp(min=1e-12) / 448.0
+            q = (pad.view(nb, 128, kb, 128) / blk.view(nb, 1, kb, 1)).view(nb * 128, kb * 128)[:N, :K]
+            out[k] = q.to(torch.float8_e4m3fn).contiguous()
+            out[k + "_scale_inv"] = blk.float().contiguous()
+        else:
+            out[k] = v.contiguous()
+    save_file(out, os.path.join(path, "model-00001-of-00001.safetensors"))
+    d = cfg.to_dict()
+    d["quantization_config"] = {"quant_method": "fp8", "weight_block_size": [128, 128]}
+    d["architectures"] = ["DeepseekV3ForCausalLM"]
+    with open(os.path.join(path, "config.json"), "w") as f:
+        json.dump(d, f)

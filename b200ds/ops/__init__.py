@@ -1,0 +1,291 @@
+"""Op surface of the engine.
+
+Every function takes plain tensors / weight containers.  CUDA tensors run the
+hand-written sm_100a kernels of the in-tree extension (``b200ds._C``); a CUDA
+call with the extension missing raises (no silent fallback).  CPU tensors run
+the fp32 references in :mod:`b200ds.ops.ref`, which is how the engine is
+tested without a GPU.  ``set_impl("torch")`` selects the library baseline on
+the GPU (cuBLAS block-scaled GEMM via torch._scaled_mm, NCCL collectives),
+the comparison arm for the benchmarks.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from . import ref
+from .quant import MXFP8Tensor, quant_mxfp8_ref, dequant_mxfp8
+
+_IMPL = "native"
+
+
+def set_impl(impl: str) -> None:
+    assert impl in ("native", "torch")
+    global _IMPL
+    _IMPL = impl
+
+
+def get_impl() -> str:
+    return _IMPL
+
+
+def _native():
+    from . import cuda as _c
+    return _c
+
+
+def _use_native(t: torch.Tensor) -> bool:
+    return t.is_cuda and _IMPL == "native"
+
+
+def _use_baseline(t: torch.Tensor) -> bool:
+    return t.is_cuda and _IMPL == "torch"
+
+
+@dataclass
+class QAct:
+    """Activation quantized to MXFP8 (q e4m3 [T, K], sf packed sf128x4),
+    optionally with the un-quantized bf16/fp32 copy ``hf``."""
+    q: torch.Tensor
+    sf: torch.Tensor
+    hf: Optional[torch.Tensor] = None
+
+    @property
+    def shape(self):
+        return self.q.shape
+
+
+@dataclass
+class ExpertWeights:
+    """Stacked local experts.  w13 [E, 2I, h] (gate rows then up rows),
+    w2 [E, h, I]; either float tensors or MXFP8 (data + per-expert sf)."""
+    first: int
+    count: int
+    w13: object
+    w2: object
+    inter: int
+
+
+def to_float(x) -> torch.Tensor:
+    if isinstance(x, QAct):
+        if x.hf is not None:
+            return x.hf.float()
+        return dequant_mxfp8(x.q, x.sf)
+    return x.float()
+
+
+def quant(x: torch.Tensor) -> QAct:
+    if _use_native(x):
+        return _native().quant(x)
+    q, sf = quant_mxfp8_ref(x.float())
+    return QAct(q, sf, None)
+
+
+# ---------------------------------------------------------------------------
+# norms
+# ---------------------------------------------------------------------------
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    if _use_native(x):
+        return _native().rmsnorm(x, w, eps)
+    if _use_baseline(x):
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(x.dtype)
+    return ref.rmsnorm(x, w, eps)
+
+
+def rmsnorm_act(x: torch.Tensor, w: torch.Tensor, eps: float, next_linear=None, keep_hf: bool = True):
+    """RMSNorm producing the operand format the next linear consumes."""
+    if next_linear is not None and getattr(next_linear, "quantized", False):
+        if _use_native(x):
+            return _native().rmsnorm_quant(x, w, eps, keep_hf)
+        y = rmsnorm(x, w, eps)
+        a = quant(y)
+        a.hf = y if keep_hf else None
+        return a
+    return rmsnorm(x, w, eps)
+
+
+def allreduce_add_rmsnorm(a: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float,
+                          ps, kind: str, next_linear=None):
+    """All-reduce the rank-partial output ``a`` over the TP group, add it to
+    the residual stream, RMSNorm, and quantize for ``next_linear``.
+    Returns (normalized activation, new residual)."""
+    if a.is_cuda and ps.tp_size > 1 and _IMPL == "native":
+        return _native().allreduce_add_rmsnorm(a, residual, w, eps, ps, next_linear)
+    if ps.tp_size > 1 or (kind == "ffn" and ps.ep_size > 1):
+        if ps.tp_size > 1:
+            ps.tp_all_reduce(a)
+        else:
+            ps.ep_all_reduce(a)
+    if a.is_cuda:
+        if _IMPL == "native":
+            return _native().add_rmsnorm_act(a, residual, w, eps, next_linear)
+        residual = (residual.float() + a.float()).to(residual.dtype)
+        return rmsnorm_act(residual, w, eps, next_linear), residual
+    residual = residual.float() + a.float()
+    return rmsnorm_act(residual, w, eps, next_linear), residual
+
+
+# ---------------------------------------------------------------------------
+# GEMM
+# ---------------------------------------------------------------------------
+
+def linear(x, w, out_dtype=torch.bfloat16) -> torch.Tensor:
+    if isinstance(w, MXFP8Tensor):
+        a = x if isinstance(x, QAct) else quant(x)
+        if a.q.is_cuda:
+            if _IMPL == "native":
+                return _native().gemm(a, w, out_dtype)
+            from . import baseline
+            return baseline.gemm(a, w, out_dtype)
+        return ref.gemm_mxfp8(a.q, a.sf, w.data, w.sf).to(out_dtype)
+    xf = to_float(x)
+    if xf.is_cuda:
+        return (xf.to(w.dtype) @ w.T).to(out_dtype)
+    return (xf @ w.float().T).to(out_dtype)
+
+
+def gate_up_swiglu(x, gate_up) -> object:
+    """silu(x Wg^T) * (x Wu^T) for a [2I, h] gate_up weight; returns the
+    operand the down projection consumes (QAct for quantized weights)."""
+    if gate_up.quantized:
+        a = x if isinstance(x, QAct) else quant(x)
+        if a.q.is_cuda and _IMPL == "native":
+            return _native().gemm_swiglu_quant(a, gate_up.w)
+        y = linear(a, gate_up.w, torch.float32)
+        h = ref.swiglu(y)
+        return quant(h.to(torch.bfloat16) if h.is_cuda else h)
+    y = gate_up(x, out_dtype=torch.float32)
+    return ref.swiglu(y)
+
+
+# ---------------------------------------------------------------------------
+# rope / kv cache / attention
+# ---------------------------------------------------------------------------
+
+def rope(x: torch.Tensor, pos: torch.Tensor, table: torch.Tensor) -> torch.Tensor:
+    if _use_native(x):
+        return _native().rope(x, pos, table)
+    return ref.rope(x, pos, table)
+
+
+def kv_store(kv_a: torch.Tensor, ln_w: torch.Tensor, eps: float, table: torch.Tensor, pos: torch.Tensor,
+             cache: torch.Tensor, slots: torch.Tensor, kv_scale: float, kv_lora: int) -> None:
+    """cache[slots] = quant([rmsnorm(kv_a[:, :kv_lora]) | rope(kv_a[:, kv_lora:])] / kv_scale)."""
+    if _use_native(kv_a):
+        return _native().kv_store(kv_a, ln_w, eps, table, pos, cache, slots, kv_scale, kv_lora)
+    ckv = ref.rmsnorm(kv_a[:, :kv_lora], ln_w, eps)
+    kpe = ref.rope(kv_a[:, kv_lora:], pos, table)
+    if cache.dtype == torch.float8_e4m3fn:
+        cache[slots.long()] = ref.kv_quant(ckv, kpe, kv_scale)
+    else:
+        cache[slots.long()] = (torch.cat([ckv, kpe], -1) / kv_scale).to(cache.dtype)
+
+
+def absorb_q(q_nope: torch.Tensor, w_uk: torch.Tensor) -> torch.Tensor:
+    """[T, H, nope] x [H, nope, L] -> [T, H, L]."""
+    if q_nope.is_cuda:
+        return torch.bmm(q_nope.transpose(0, 1).to(w_uk.dtype), w_uk).transpose(0, 1)
+    return torch.einsum("thd,hdc->thc", q_nope.float(), w_uk.float())
+
+
+def absorb_o(o_lat: torch.Tensor, w_uv: torch.Tensor) -> torch.Tensor:
+    """[T, H, L] x [H, v, L] -> [T, H*v]."""
+    T, H, L = o_lat.shape
+    if o_lat.is_cuda:
+        return torch.bmm(o_lat.transpose(0, 1).to(w_uv.dtype), w_uv.transpose(1, 2)).transpose(0, 1).reshape(T, -1)
+    return torch.einsum("thc,hdc->thd", o_lat.float(), w_uv.float()).reshape(T, -1)
+
+
+def mla_attention(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size, topk=None):
+    if _use_native(q_abs):
+        return _native().mla_attention(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size, topk)
+    out = ref.mla_attention(q_abs, q_pe, cache, kv_scale, fb.block_table, fb.seq_lens, fb.q_seq,
+                            fb.positions, softmax_scale, page_size, topk)
+    return out.to(q_abs.dtype) if q_abs.is_cuda else out
+
+
+def index_k_store(k: torch.Tensor, cache: torch.Tensor, scale: torch.Tensor, slots: torch.Tensor) -> None:
+    """Indexer key cache: per-token e4m3 with an fp32 scale."""
+    if cache.dtype == torch.float8_e4m3fn:
+        amax = k.float().abs().amax(-1).clamp(min=1e-12)
+        s = amax / 448.0
+        cache[slots.long()] = (k.float() / s.unsqueeze(-1)).to(cache.dtype)
+        scale[slots.long()] = s
+    else:
+        cache[slots.long()] = k.to(cache.dtype)
+        scale[slots.long()] = 1.0
+
+
+def indexer_topk(q, w, k_cache, k_scale, fb, page_size, topk):
+    if _use_native(q):
+        return _native().indexer_topk(q, w, k_cache, k_scale, fb, page_size, topk)
+    return ref.indexer_scores(q, w, k_cache, k_scale, fb.block_table, fb.q_seq, fb.positions, page_size, topk)
+
+
+# ---------------------------------------------------------------------------
+# MoE
+# ---------------------------------------------------------------------------
+
+def router(h, gate: torch.Tensor, bias: torch.Tensor, cfg):
+    x = to_float(h) if not (isinstance(h, QAct) and h.hf is not None and h.hf.is_cuda) else h.hf
+    if _use_native(x):
+        return _native().router(x, gate, bias, cfg)
+    logits = x.float() @ gate.float().T
+    return ref.router_topk(logits, bias, cfg.num_experts_per_tok, cfg.n_group, cfg.topk_group,
+                           cfg.routed_scaling_factor, cfg.norm_topk_prob)
+
+
+def moe_experts(h, w: torch.Tensor, ids: torch.Tensor, ex: ExpertWeights, out_dtype=torch.float32):
+    """Local-expert part of the MoE: sum_k w[t,k] * expert_{ids[t,k]}(h[t]) over
+    the experts this rank owns (others contribute on their ranks)."""
+    if isinstance(ex.w13, MXFP8Tensor) and (h.q if isinstance(h, QAct) else h).is_cuda:
+        if _IMPL == "native":
+            return _native().moe_experts(h, w, ids, ex, out_dtype)
+        from . import baseline
+        return baseline.moe_experts(h if isinstance(h, QAct) else quant(h), w, ids, ex, out_dtype)
+    xf = to_float(h)
+    T = xf.shape[0]
+    out = torch.zeros(T, xf.shape[1], dtype=torch.float32, device=xf.device)
+    quantized = isinstance(ex.w13, MXFP8Tensor)
+    for e in range(ex.count):
+        gid = ex.first + e
+        hit = (ids == gid)
+        tok = hit.any(-1).nonzero().flatten()
+        if tok.numel() == 0:
+            continue
+        we = (w * hit).sum(-1)[tok].unsqueeze(-1)
+        if quantized:
+            a = QAct(*quant_mxfp8_ref(xf[tok]))
+            w13 = MXFP8Tensor(ex.w13.data[e], ex.w13.sf[e])
+            w2 = MXFP8Tensor(ex.w2.data[e], ex.w2.sf[e])
+            y = ref.swiglu(ref.gemm_mxfp8(a.q, a.sf, w13.data, w13.sf))
+            a2 = QAct(*quant_mxfp8_ref(y))
+            o = ref.gemm_mxfp8(a2.q, a2.sf, w2.data, w2.sf)
+        else:
+            y = ref.swiglu(xf[tok] @ ex.w13[e].float().T)
+            o = y @ ex.w2[e].float().T
+        out.index_add_(0, tok, we * o)
+    return out.to(out_dtype)
+
+
+# ---------------------------------------------------------------------------
+# LM head / sampling
+# ---------------------------------------------------------------------------
+
+def lm_head_logits(x: torch.Tensor, head: torch.Tensor, ps) -> torch.Tensor:
+    if x.is_cuda:
+        logits = (x.to(head.dtype) @ head.T).float()
+    else:
+        logits = x.float() @ head.float().T
+    return ps.tp_all_gather(logits, dim=-1)
+
+
+def sample(logits: torch.Tensor, temperature, top_p, top_k, uniform) -> torch.Tensor:
+    if _use_native(logits):
+        return _native().sample(logits, temperature, top_p, top_k, uniform)
+    return ref.sample(logits, temperature, top_p, top_k, uniform)

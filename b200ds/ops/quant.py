@@ -1,0 +1,187 @@
+"""Block-scaled weight / activation formats and their PyTorch reference math.
+
+MXFP8 (used for every dense / expert GEMM operand):
+  * data: float8_e4m3fn [R, K];
+  * scale: one UE8M0 byte per 32 consecutive K elements of a row
+    (value 2**(byte-127)), chosen as the smallest power of two with
+    amax/scale <= 448 so quantization never saturates;
+  * the scale bytes are stored in the tcgen05 scale-factor tile layout
+    ("sf128x4"): rows are padded to a multiple of 128 and K/32 scale columns
+    are grouped by 4; chunk (row_block, k_chunk) is 512 contiguous bytes in
+    which row rb*128 + 32*j + i, scale column 4*kc + c sits at byte
+    16*i + 4*j + c.  A GEMM stage of 128 rows x 128 K copies one chunk
+    straight into tensor memory with `tcgen05.cp ... 32x128b.warpx4`.
+
+NVFP4 (routed experts in the NVFP4 configuration): e2m1 pairs packed in bytes,
+one e4m3 scale per 16 K elements, one fp32 global scale per tensor.
+
+DeepSeek checkpoints ship e4m3 weights with fp32 128x128 block scales
+(`weight_scale_inv`); :func:`mxfp8_from_block128` converts them at load time.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+E4M3_MAX = 448.0
+E2M1_MAX = 6.0
+SF_ROWS = 128      # rows per scale-factor chunk
+SF_KCHUNK = 128    # K elements per scale-factor chunk (4 blocks of 32)
+
+
+def round_up(x: int, m: int) -> int:
+    return (x + m - 1) // m * m
+
+
+# ---------------------------------------------------------------------------
+# UE8M0 scale selection
+# ---------------------------------------------------------------------------
+
+def ue8m0_ceil_exponent(ratio: torch.Tensor) -> torch.Tensor:
+    """ceil(log2(ratio)) for ratio > 0 computed exactly from float32 bits;
+    ratio == 0 maps to -127.  Result clamped to [-127, 127]."""
+    r = ratio.float().contiguous()
+    bits = r.view(torch.int32)
+    e = ((bits >> 23) & 0xFF) - 127
+    mant = bits & 0x7FFFFF
+    e = torch.where(mant != 0, e + 1, e)
+    e = torch.where(r > 0, e, torch.full_like(e, -127))
+    return e.clamp(-127, 127)
+
+
+# ---------------------------------------------------------------------------
+# sf128x4 layout packing
+# ---------------------------------------------------------------------------
+
+def sf_packed_size(rows: int, k: int) -> int:
+    return round_up(rows, SF_ROWS) * (k // 32)
+
+
+def pack_sf(sf: torch.Tensor) -> torch.Tensor:
+    """[R, K/32] uint8 (row-major) -> flat sf128x4 layout (uint8)."""
+    R, KB = sf.shape
+    assert KB % 4 == 0, "K must be a multiple of 128"
+    Rp = round_up(R, SF_ROWS)
+    if Rp != R:
+        sf = torch.cat([sf, torch.full((Rp - R, KB), 127, dtype=sf.dtype, device=sf.device)], 0)
+    # [rb, j, i, kc, c] -> [rb, kc, i, j, c]
+    t = sf.view(Rp // 128, 4, 32, KB // 4, 4).permute(0, 3, 2, 1, 4).contiguous()
+    return t.view(-1)
+
+
+def unpack_sf(packed: torch.Tensor, rows: int, k: int) -> torch.Tensor:
+    """Inverse of :func:`pack_sf` -> [rows, K/32] uint8."""
+    Rp = round_up(rows, SF_ROWS)
+    KB = k // 32
+    t = packed.view(Rp // 128, KB // 4, 32, 4, 4).permute(0, 3, 2, 1, 4).contiguous()
+    return t.view(Rp, KB)[:rows]
+
+
+# ---------------------------------------------------------------------------
+# MXFP8 tensors
+# ---------------------------------------------------------------------------
+
+@dataclass
+class MXFP8Tensor:
+    """Row-wise MXFP8 matrix: data [R, K] e4m3, scales in sf128x4 layout."""
+    data: torch.Tensor
+    sf: torch.Tensor
+
+    @property
+    def shape(self):
+        return self.data.shape
+
+    def dequant(self) -> torch.Tensor:
+        return dequant_mxfp8(self.data, self.sf)
+
+
+def quant_mxfp8_ref(x: torch.Tensor, packed: bool = True):
+    """Reference MXFP8 quantization of x [R, K] (K % 128 == 0).
+
+    Returns (data e4m3 [R, K], scales uint8 packed sf128x4 or [R, K/32])."""
+    R, K = x.shape
+    xb = x.float().view(R, K // 32, 32)
+    amax = xb.abs().amax(-1)
+    e = ue8m0_ceil_exponent(amax / E4M3_MAX)
+    inv = torch.pow(2.0, -e.float()).unsqueeze(-1)
+    q = (xb * inv).view(R, K).to(torch.float8_e4m3fn)
+    sf = (e + 127).to(torch.uint8)
+    return q, (pack_sf(sf) if packed else sf)
+
+
+def dequant_mxfp8(q: torch.Tensor, sf: torch.Tensor, packed: bool = True) -> torch.Tensor:
+    R, K = q.shape
+    s = unpack_sf(sf, R, K) if packed else sf
+    scale = torch.pow(2.0, s.float() - 127.0)
+    return (q.float().view(R, K // 32, 32) * scale.unsqueeze(-1)).view(R, K)
+
+
+def mxfp8_from_block128(w: torch.Tensor, scale_inv: torch.Tensor) -> MXFP8Tensor:
+    """Convert a DeepSeek fp8 weight [N, K] with fp32 128x128 block scales
+    [ceil(N/128), ceil(K/128)] to MXFP8 (dequantize, requantize per 32)."""
+    N, K = w.shape
+    s = scale_inv.float().repeat_interleave(128, 0)[:N].repeat_interleave(128, 1)[:, :K]
+    full = w.float() * s
+    q, sf = quant_mxfp8_ref(full)
+    return MXFP8Tensor(q, sf)
+
+
+# ---------------------------------------------------------------------------
+# NVFP4
+# ---------------------------------------------------------------------------
+
+_E2M1_GRID = torch.tensor([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0])
+
+
+def _e2m1_encode(v: torch.Tensor) -> torch.Tensor:
+    """Round |v| <= 6 to the nearest e2m1 value (ties to even code); 4-bit codes."""
+    a = v.abs().clamp(max=E2M1_MAX)
+    grid = _E2M1_GRID.to(v.device)
+    d = (a.unsqueeze(-1) - grid).abs()
+    # tie-break towards even code index: add a tiny bias to odd indices
+    bias = (torch.arange(8, device=v.device) % 2).float() * 1e-7
+    code = (d + bias).argmin(-1)
+    sign = (v < 0) & (code != 0)
+    return (code | (sign.to(torch.int64) << 3)).to(torch.uint8)
+
+
+def _e2m1_decode(c: torch.Tensor) -> torch.Tensor:
+    grid = _E2M1_GRID.to(c.device)
+    v = grid[(c & 7).long()]
+    return torch.where((c & 8) != 0, -v, v)
+
+
+@dataclass
+class NVFP4Tensor:
+    data: torch.Tensor      # uint8 [R, K/2], low nibble = even element
+    sf: torch.Tensor        # e4m3 [R, K/16] (plain row-major)
+    global_scale: torch.Tensor  # fp32 scalar
+
+    def dequant(self) -> torch.Tensor:
+        return dequant_nvfp4(self.data, self.sf, self.global_scale)
+
+
+def quant_nvfp4_ref(x: torch.Tensor, global_scale: Optional[torch.Tensor] = None) -> NVFP4Tensor:
+    R, K = x.shape
+    xf = x.float()
+    if global_scale is None:
+        global_scale = (xf.abs().amax() / (E4M3_MAX * E2M1_MAX)).clamp(min=1e-12)
+    xb = xf.view(R, K // 16, 16)
+    amax = xb.abs().amax(-1)
+    s = (amax / (E2M1_MAX * global_scale)).to(torch.float8_e4m3fn)
+    denom = (s.float() * global_scale).unsqueeze(-1)
+    v = torch.where(denom > 0, xb / denom, torch.zeros_like(xb)).view(R, K)
+    codes = _e2m1_encode(v)
+    packed = (codes[:, 0::2] | (codes[:, 1::2] << 4)).to(torch.uint8)
+    return NVFP4Tensor(packed, s, global_scale.float().reshape(()))
+
+
+def dequant_nvfp4(data: torch.Tensor, sf: torch.Tensor, g: torch.Tensor) -> torch.Tensor:
+    R = data.shape[0]
+    K = data.shape[1] * 2
+    lo = _e2m1_decode(data & 0xF)
+    hi = _e2m1_decode(data >> 4)
+    v = torch.stack([lo, hi], -1).view(R, K)
+    return (v.view(R, K // 16, 16) * sf.float().unsqueeze(-1) * g.float()).view(R, K)
