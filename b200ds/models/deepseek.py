@@ -140,8 +140,9 @@ class DeepseekModel:
         T = fb.num_tokens
         qkv = aw.qkv_a(h, out_dtype=torch.float32 if self.device.type == "cpu" else torch.bfloat16)
         ql = c.q_lora_rank
-        q_lat = ops.rmsnorm(qkv[:, :ql], aw.q_a_ln, c.rms_norm_eps)
-        ops.kv_store(qkv[:, ql:], aw.kv_a_ln, c.rms_norm_eps, self.rope_table, fb.positions,
+        q_lat = ops.rmsnorm_act(qkv[:, :ql], aw.q_a_ln, c.rms_norm_eps, aw.q_b,
+                                keep_hf=bool(c.index_n_heads))
+        ops.kv_store(qkv[:, ql:ql + c.kv_cache_dim], aw.kv_a_ln, c.rms_norm_eps, self.rope_table, fb.positions,
                      self.kv_cache[i], fb.out_slots, self.kv_scale[i], c.kv_lora_rank)
         q = aw.q_b(q_lat, out_dtype=torch.float32 if self.device.type == "cpu" else torch.bfloat16)
         q = q.view(T, self.heads, c.qk_head_dim)
@@ -188,8 +189,7 @@ class DeepseekModel:
     def forward(self, fb: ForwardBatch) -> torch.Tensor:
         """Returns logits [B, V] (full vocab) for each sequence's last token."""
         c = self.cfg
-        x = self.embed[fb.input_ids.long()].float() if self.device.type == "cpu" else self.embed[fb.input_ids.long()]
-        residual = x
+        residual = self.embed[fb.input_ids.long()].float()      # fp32 residual stream
         h = ops.rmsnorm_act(residual, self.layers[0].in_ln, c.rms_norm_eps, self.layers[0].attn.qkv_a)
         for i, lw in enumerate(self.layers):
             a = self._attention(i, lw, h, fb)

@@ -22,10 +22,13 @@ from .deepseek import AttnWeights, DeepseekModel, DenseWeights, LayerWeights, Li
 
 
 def _quantize(w: torch.Tensor, fmt: str, device) -> object:
-    """float weight [N, K] -> serving format on device."""
+    """float weight [N, K] -> serving format on device (MXFP8 rows padded
+    with zeros to a multiple of 128, the GEMM's weight tile)."""
     if fmt in ("fp32", "bf16"):
         return w.to(device=device, dtype=torch.float32 if fmt == "fp32" else torch.bfloat16)
     if fmt == "mxfp8":
+        if w.shape[0] % 128:
+            w = torch.cat([w, torch.zeros(128 - w.shape[0] % 128, w.shape[1], dtype=w.dtype)], 0)
         wd = w.to(device)
         if wd.is_cuda:
             from .. import ops

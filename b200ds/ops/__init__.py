@@ -102,6 +102,9 @@ def rmsnorm_act(x: torch.Tensor, w: torch.Tensor, eps: float, next_linear=None, 
     if next_linear is not None and getattr(next_linear, "quantized", False):
         if _use_native(x):
             return _native().rmsnorm_quant(x, w, eps, keep_hf)
+        if x.is_cuda:
+            from . import baseline
+            return baseline.rmsnorm_quant(x, w, eps, keep_hf)
         y = rmsnorm(x, w, eps)
         a = quant(y)
         a.hf = y if keep_hf else None

@@ -1,0 +1,231 @@
+"""CUDA implementations of the op surface: thin wrappers over b200ds._C.
+
+Importing this module on a machine with a GPU but without the built
+extension raises: there is no silent fallback.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from .quant import MXFP8Tensor, round_up
+
+try:
+    from .. import _C  # noqa: F401
+except ImportError as e:  # pragma: no cover - only on a box without the build
+    raise ImportError("b200ds native extension is not built: run `python setup.py build_ext --inplace` "
+                      "(or __graft_entry__.build())") from e
+
+from .. import _C
+
+
+def _qact():
+    from . import QAct
+    return QAct
+
+
+def sf_bytes(rows: int, k: int) -> int:
+    return round_up(rows, 128) * (k // 32)
+
+
+def alloc_qact(rows: int, k: int, device) -> "QAct":
+    QAct = _qact()
+    q = torch.empty(rows, k, dtype=torch.float8_e4m3fn, device=device)
+    sf = torch.empty(sf_bytes(rows, k), dtype=torch.uint8, device=device)
+    return QAct(q, sf, None)
+
+
+# ---------------------------------------------------------------------------
+def quant(x: torch.Tensor):
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    if x2.dtype not in (torch.bfloat16, torch.float32):
+        x2 = x2.to(torch.bfloat16)
+    a = alloc_qact(x2.shape[0], x2.shape[1], x2.device)
+    _C.quant(x2, a.q, a.sf)
+    return a
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    y = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    xx = x if x.dtype in (torch.bfloat16, torch.float32) else x.to(torch.bfloat16)
+    _C.rmsnorm(xx, None, w, eps, y, None, None)
+    return y
+
+
+def rmsnorm_quant(x: torch.Tensor, w: torch.Tensor, eps: float, keep_hf: bool = True):
+    a = alloc_qact(x.shape[0], x.shape[1], x.device)
+    y = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device) if keep_hf else None
+    _C.rmsnorm(x, None, w, eps, y, a.q, a.sf)
+    a.hf = y
+    return a
+
+
+def add_rmsnorm_act(a: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float, next_linear=None):
+    """residual (fp32, in place) += a; returns (normalized act, residual)."""
+    if residual.dtype != torch.float32:
+        residual = residual.float()
+    a2 = a if a.dtype == torch.bfloat16 else a.to(torch.bfloat16)
+    rows, K = residual.shape
+    quantized = next_linear is not None and getattr(next_linear, "quantized", False)
+    y = torch.empty(rows, K, dtype=torch.bfloat16, device=a.device)
+    if quantized:
+        q = alloc_qact(rows, K, a.device)
+        _C.rmsnorm(a2, residual, w, eps, y, q.q, q.sf)
+        q.hf = y
+        return q, residual
+    _C.rmsnorm(a2, residual, w, eps, y, None, None)
+    return y, residual
+
+
+def allreduce_add_rmsnorm(a, residual, w, eps, ps, next_linear=None):
+    from . import comm
+    a = comm.all_reduce(a, ps)
+    return add_rmsnorm_act(a, residual, w, eps, next_linear)
+
+
+# ---------------------------------------------------------------------------
+def _gemm_raw(a, w: MXFP8Tensor, out: torch.Tensor, epi: int, splits: int = 1, pdl: bool = False):
+    T, K = a.q.shape
+    N = w.data.shape[0]
+    _C.gemm(w.data, w.sf, 0, a.q, a.sf, N, T, K, epi, splits, out, out.stride(0), None, None, 0, 0, 0,
+            None, None, 0, None, None, pdl)
+
+
+def choose_splits(T: int, N: int, K: int) -> int:
+    """Split-K factor so small-token GEMMs still cover the 148 SMs."""
+    tiles = (N // 128) * max(1, (T + 127) // 128)
+    if tiles >= 148 or T > 256:
+        return 1
+    ktiles = K // 128
+    s = 1
+    while tiles * s * 2 <= 2 * 148 and s * 2 <= ktiles // 4:
+        s *= 2
+    return s
+
+
+def gemm(a, w: MXFP8Tensor, out_dtype=torch.bfloat16) -> torch.Tensor:
+    T, K = a.q.shape
+    N = w.data.shape[0]
+    assert w.data.shape[1] == K, (w.data.shape, a.q.shape)
+    splits = choose_splits(T, N, K)
+    if splits > 1 or out_dtype == torch.float32:
+        out = torch.zeros(T, N, dtype=torch.float32, device=a.q.device)
+        _gemm_raw(a, w, out, 1, splits)
+        return out if out_dtype == torch.float32 else out.to(out_dtype)
+    out = torch.empty(T, N, dtype=torch.bfloat16, device=a.q.device)
+    _gemm_raw(a, w, out, 0)
+    return out
+
+
+def gemm_swiglu_quant(a, w: MXFP8Tensor):
+    """MXFP8 act [T, K] x gate_up [2I, K] -> MXFP8(silu(g) * u) [T, I]."""
+    T, K = a.q.shape
+    I = w.data.shape[0] // 2
+    o = alloc_qact(T, I, a.q.device)
+    _C.gemm(w.data, w.sf, 0, a.q, a.sf, 2 * I, T, K, 2, 1, None, 0, o.q, o.sf, I, I, 0, None, None, 0, None, None,
+            False)
+    return o
+
+
+# ---------------------------------------------------------------------------
+def rope(x: torch.Tensor, pos: torch.Tensor, table: torch.Tensor) -> torch.Tensor:
+    """In-place rotation of x [T, H, d] (any row strides, unit inner stride)."""
+    if x.dim() == 2:
+        x3 = x.unsqueeze(1)
+    else:
+        x3 = x
+    _C.rope(x3, pos, table)
+    return x
+
+
+def kv_store(kv_a, ln_w, eps, table, pos, cache, slots, kv_scale, kv_lora):
+    _C.kv_store(kv_a, ln_w, eps, pos, table, slots, cache.view(torch.uint8), kv_scale, kv_lora)
+
+
+def mla_attention(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size, topk=None):
+    T, H, L = q_abs.shape
+    out = torch.empty(T, H, L, dtype=torch.bfloat16, device=q_abs.device)
+    qa = q_abs.to(torch.bfloat16).contiguous()
+    qp = q_pe.to(torch.bfloat16).contiguous()
+    _C.mla_simt(qa, qp, cache.view(torch.uint8), kv_scale, fb.block_table, fb.q_seq, fb.positions, topk,
+                page_size, softmax_scale, out)
+    return out
+
+
+# ---------------------------------------------------------------------------
+def router(x: torch.Tensor, gate: torch.Tensor, bias: torch.Tensor, cfg):
+    logits = torch.matmul(x.float(), gate.float().t()) if gate.dtype == torch.float32 else \
+        torch.matmul(x.to(gate.dtype), gate.t()).float()
+    T = logits.shape[0]
+    K = cfg.num_experts_per_tok
+    w = torch.empty(T, K, dtype=torch.float32, device=x.device)
+    ids = torch.empty(T, K, dtype=torch.int32, device=x.device)
+    _C.router(logits.contiguous(), bias.float(), cfg.n_group, cfg.topk_group, K, cfg.routed_scaling_factor,
+              cfg.norm_topk_prob, w, ids)
+    return w, ids
+
+
+def moe_experts(h, w: torch.Tensor, ids: torch.Tensor, ex, out_dtype=torch.bfloat16) -> torch.Tensor:
+    """Local-expert MoE: align -> gather -> FC1 (SwiGLU+quant) -> FC2
+    (routing-weighted) -> combine.  Host-synchronisation free: buffers are
+    sized for the worst case (every pair local)."""
+    from . import QAct
+    a = h if isinstance(h, QAct) else quant(h)
+    T, Hd = a.q.shape
+    K = ids.shape[1]
+    E = ex.count
+    dev = a.q.device
+    I = ex.inter
+    max_rows = round_up(T * K, 128) + E * 128   # 128-aligned segments
+    seg_start = torch.empty(E, dtype=torch.int32, device=dev)
+    seg_count = torch.empty(E, dtype=torch.int32, device=dev)
+    row_token = torch.full((max_rows,), -1, dtype=torch.int32, device=dev)
+    row_weight = torch.zeros(max_rows, dtype=torch.float32, device=dev)
+    pair_row = torch.empty(T, K, dtype=torch.int32, device=dev)
+    total = torch.empty(1, dtype=torch.int32, device=dev)
+    _C.moe_align(ids, w.float().contiguous(), ex.first, E, seg_start, seg_count, row_token, row_weight, pair_row, total)
+    xs = alloc_qact(max_rows, Hd, dev)
+    _C.moe_gather(a.q, a.sf, row_token, max_rows, xs.q, xs.sf)
+    hq = alloc_qact(max_rows, I, dev)
+    max_per = min(T, max_rows)   # an expert receives each token at most once
+    w13, w2 = ex.w13, ex.w2
+    _C.gemm(w13.data, w13.sf, w13.sf.stride(0) if w13.sf.dim() > 1 else 0, xs.q, xs.sf, 2 * I, max_rows, Hd, 2, 1,
+            None, 0, hq.q, hq.sf, I, I, E, seg_start, seg_count, max_per, None, None, False)
+    y = torch.empty(max_rows, Hd, dtype=torch.bfloat16, device=dev)
+    _C.gemm(w2.data, w2.sf, w2.sf.stride(0) if w2.sf.dim() > 1 else 0, hq.q, hq.sf, Hd, max_rows, I, 3, 1,
+            y, Hd, None, None, 0, 0, E, seg_start, seg_count, max_per, row_weight, None, False)
+    out = torch.empty(T, Hd, dtype=out_dtype, device=dev)
+    _C.moe_combine(y, pair_row, None, out)
+    return out
+
+
+# ---------------------------------------------------------------------------
+def indexer_topk(q, w, k_cache, k_scale, fb, page_size, topk):
+    from . import ref
+    return ref.indexer_scores(q, w, k_cache, k_scale, fb.block_table, fb.q_seq, fb.positions, page_size, topk)
+
+
+def sample(logits, temperature, top_p, top_k, uniform):
+    """Vectorised temperature / top-k / top-p sampling with given uniforms."""
+    greedy = temperature <= 0
+    t = torch.where(greedy, torch.ones_like(temperature), temperature)
+    p = torch.softmax(logits.float() / t.unsqueeze(-1), -1)
+    sp, si = p.sort(-1, descending=True)
+    V = p.shape[-1]
+    ar = torch.arange(V, device=p.device).unsqueeze(0)
+    keep = torch.ones_like(sp, dtype=torch.bool)
+    k = top_k.long().unsqueeze(-1)
+    keep &= (k <= 0) | (ar < k)
+    c = sp.cumsum(-1)
+    keep &= (c - sp) < top_p.unsqueeze(-1)
+    sp = torch.where(keep, sp, torch.zeros_like(sp))
+    c = sp.cumsum(-1)
+    u = (uniform * c[:, -1]).unsqueeze(-1)
+    j = torch.searchsorted(c, u).clamp(max=V - 1)
+    tok = si.gather(1, j).squeeze(-1)
+    return torch.where(greedy, logits.argmax(-1), tok)

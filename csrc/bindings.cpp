@@ -1,0 +1,182 @@
+// Python bindings of the native kernels (module b200ds._C).
+// Every entry point validates devices / dtypes / alignment and launches on
+// the current CUDA stream; kernels never allocate.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "attn/attn.h"
+#include "comm/comm.h"
+#include "elementwise/elementwise.h"
+#include "gemm/gemm_mxf8.h"
+
+namespace {
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+template <typename T>
+T* ptr(const at::Tensor& t) {
+  return reinterpret_cast<T*>(t.data_ptr());
+}
+template <typename T>
+T* optr(const c10::optional<at::Tensor>& t) {
+  return t.has_value() && t->defined() ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+
+void check(int rc, const char* what) { TORCH_CHECK(rc == 0, what, " failed with code ", rc); }
+
+void check_cuda(const at::Tensor& t, const char* n) {
+  TORCH_CHECK(t.is_cuda(), n, " must be a CUDA tensor");
+}
+
+// ---------------------------------------------------------------------------
+void rmsnorm(const at::Tensor& x, c10::optional<at::Tensor> residual, const at::Tensor& w, double eps,
+             c10::optional<at::Tensor> y, c10::optional<at::Tensor> q, c10::optional<at::Tensor> sf) {
+  check_cuda(x, "x");
+  const c10::cuda::CUDAGuard g(x.device());
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x must be 2-D row-major");
+  TORCH_CHECK(w.scalar_type() == at::kFloat, "w must be fp32");
+  const int rows = x.size(0), K = x.size(1);
+  if (residual.has_value()) TORCH_CHECK(residual->scalar_type() == at::kFloat && residual->is_contiguous(), "residual fp32");
+  const int ldy = y.has_value() ? y->stride(0) : 0;
+  check(b200_rmsnorm(x.data_ptr(), x.scalar_type() == at::kFloat, x.stride(0), optr<float>(residual), ptr<float>(w),
+                     float(eps), rows, K, optr<void>(y), ldy, optr<uint8_t>(q), optr<uint8_t>(sf), cur_stream()),
+        "rmsnorm");
+}
+
+void quant(const at::Tensor& x, at::Tensor q, at::Tensor sf) {
+  check_cuda(x, "x");
+  const c10::cuda::CUDAGuard g(x.device());
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x must be 2-D row-major");
+  check(b200_quant_mxfp8(x.data_ptr(), x.scalar_type() == at::kFloat, x.stride(0), x.size(0), x.size(1), ptr<uint8_t>(q),
+                         ptr<uint8_t>(sf), cur_stream()),
+        "quant");
+}
+
+void gemm(const at::Tensor& w, const at::Tensor& w_sf, int64_t w_sf_estride, const at::Tensor& x,
+          const at::Tensor& x_sf, int64_t nw, int64_t t, int64_t k, int64_t epi, int64_t splits,
+          c10::optional<at::Tensor> out, int64_t ldo, c10::optional<at::Tensor> q_out, c10::optional<at::Tensor> sf_out,
+          int64_t ldq, int64_t inter, int64_t num_experts, c10::optional<at::Tensor> seg_start,
+          c10::optional<at::Tensor> seg_count, int64_t max_rows, c10::optional<at::Tensor> row_weight,
+          c10::optional<at::Tensor> err, bool pdl) {
+  check_cuda(w, "w");
+  const c10::cuda::CUDAGuard g(w.device());
+  TORCH_CHECK(k % 128 == 0, "K must be a multiple of 128");
+  TORCH_CHECK(nw % 128 == 0, "weight rows must be a multiple of 128");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0,
+              "operands must be 16-byte aligned");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(x_sf.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(w_sf.data_ptr()) % 16 == 0,
+              "scales must be 16-byte aligned");
+  GemmArgs a{};
+  a.w = ptr<uint8_t>(w);
+  a.w_sf = ptr<uint8_t>(w_sf);
+  a.w_sf_estride = w_sf_estride;
+  a.x = ptr<uint8_t>(x);
+  a.x_sf = ptr<uint8_t>(x_sf);
+  a.x_rows = x.size(0);
+  a.nw = nw;
+  a.nw_total = num_experts > 0 ? nw * num_experts : w.numel() / k;
+  a.t = t;
+  a.k = k;
+  a.splits = splits;
+  a.num_experts = num_experts;
+  a.seg_start = optr<int>(seg_start);
+  a.seg_count = optr<int>(seg_count);
+  a.max_rows_per_expert = max_rows;
+  a.epi = epi;
+  a.out = optr<void>(out);
+  a.ldo = ldo;
+  a.q_out = optr<uint8_t>(q_out);
+  a.sf_out = optr<uint8_t>(sf_out);
+  a.ldq = ldq;
+  a.inter = inter;
+  a.row_weight = optr<float>(row_weight);
+  a.err = optr<uint32_t>(err);
+  a.pdl = pdl ? 1 : 0;
+  check(b200_gemm_mxf8(&a, cur_stream()), "gemm_mxf8");
+}
+
+void rope(at::Tensor x, const at::Tensor& pos, const at::Tensor& table) {
+  check_cuda(x, "x");
+  const c10::cuda::CUDAGuard g(x.device());
+  TORCH_CHECK(x.dim() == 3 && x.stride(2) == 1, "x must be [T, H, d] with unit inner stride");
+  TORCH_CHECK(pos.scalar_type() == at::kInt, "pos int32");
+  check(b200_rope(x.data_ptr(), x.scalar_type() == at::kFloat, x.stride(0), x.stride(1), x.size(0), x.size(1), x.size(2),
+                  ptr<int>(pos), ptr<float>(table), cur_stream()),
+        "rope");
+}
+
+void kv_store(const at::Tensor& kv, const at::Tensor& w, double eps, const at::Tensor& pos, const at::Tensor& table,
+              const at::Tensor& slots, at::Tensor cache, double kv_scale, int64_t L) {
+  check_cuda(kv, "kv");
+  const c10::cuda::CUDAGuard g(kv.device());
+  TORCH_CHECK(kv.dim() == 2 && kv.stride(1) == 1, "kv 2-D");
+  TORCH_CHECK(slots.scalar_type() == at::kLong, "slots int64");
+  const int R = kv.size(1) - L;
+  TORCH_CHECK(cache.size(1) == L + R, "cache width");
+  check(b200_kv_store(kv.data_ptr(), kv.scalar_type() == at::kFloat, kv.stride(0), kv.size(0), L, R, ptr<float>(w),
+                      float(eps), ptr<int>(pos), ptr<float>(table), ptr<int64_t>(slots), ptr<uint8_t>(cache),
+                      float(kv_scale), cur_stream()),
+        "kv_store");
+}
+
+void router(const at::Tensor& logits, const at::Tensor& bias, int64_t G, int64_t topk_group, int64_t K, double scaling,
+            bool renorm, at::Tensor w_out, at::Tensor id_out) {
+  check_cuda(logits, "logits");
+  const c10::cuda::CUDAGuard g(logits.device());
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.is_contiguous(), "logits fp32 contiguous");
+  check(b200_router(ptr<float>(logits), ptr<float>(bias), logits.size(0), logits.size(1), G, topk_group, K, float(scaling),
+                    renorm ? 1 : 0, ptr<float>(w_out), ptr<int>(id_out), cur_stream()),
+        "router");
+}
+
+void moe_align(const at::Tensor& ids, const at::Tensor& w, int64_t first, int64_t E, at::Tensor seg_start,
+               at::Tensor seg_count, at::Tensor row_token, at::Tensor row_weight, at::Tensor pair_row,
+               at::Tensor total_rows) {
+  check_cuda(ids, "ids");
+  const c10::cuda::CUDAGuard g(ids.device());
+  check(b200_moe_align(ptr<int>(ids), ptr<float>(w), ids.size(0), ids.size(1), first, E, ptr<int>(seg_start),
+                       ptr<int>(seg_count), ptr<int>(row_token), ptr<float>(row_weight), ptr<int>(pair_row),
+                       ptr<int>(total_rows), cur_stream()),
+        "moe_align");
+}
+
+void moe_gather(const at::Tensor& xq, const at::Tensor& xsf, const at::Tensor& row_token, int64_t rows_total,
+                at::Tensor dq, at::Tensor dsf) {
+  check_cuda(xq, "xq");
+  const c10::cuda::CUDAGuard g(xq.device());
+  check(b200_moe_gather(ptr<uint8_t>(xq), ptr<uint8_t>(xsf), ptr<int>(row_token), rows_total, xq.size(1),
+                        ptr<uint8_t>(dq), ptr<uint8_t>(dsf), cur_stream()),
+        "moe_gather");
+}
+
+void moe_combine(const at::Tensor& y, const at::Tensor& pair_row, c10::optional<at::Tensor> add, at::Tensor out) {
+  check_cuda(y, "y");
+  const c10::cuda::CUDAGuard g(y.device());
+  TORCH_CHECK(y.scalar_type() == at::kBFloat16, "y bf16");
+  const int T = pair_row.size(0), K = pair_row.size(1), D = y.size(1);
+  check(b200_moe_combine(y.data_ptr(), ptr<int>(pair_row), T, K, D, optr<void>(add),
+                         add.has_value() && add->scalar_type() == at::kFloat, out.data_ptr(),
+                         out.scalar_type() == at::kFloat, cur_stream()),
+        "moe_combine");
+}
+
+}  // namespace
+
+void register_attn(pybind11::module& m);
+void register_comm(pybind11::module& m);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "b200ds native sm_100a kernels";
+  m.def("rmsnorm", &rmsnorm);
+  m.def("quant", &quant);
+  m.def("gemm", &gemm);
+  m.def("rope", &rope);
+  m.def("kv_store", &kv_store);
+  m.def("router", &router);
+  m.def("moe_align", &moe_align);
+  m.def("moe_gather", &moe_gather);
+  m.def("moe_combine", &moe_combine);
+  register_attn(m);
+  register_comm(m);
+}

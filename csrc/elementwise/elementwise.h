@@ -1,0 +1,21 @@
+// Host interface of the elementwise / routing kernels.  All take raw device
+// pointers and a stream; return 0 on success.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+int b200_rmsnorm(const void* x, int x_is_f32, int ldx, float* residual, const float* w, float eps, int rows, int K,
+                 void* y, int ldy, uint8_t* q, uint8_t* sf, cudaStream_t st);
+int b200_quant_mxfp8(const void* x, int x_is_f32, int ldx, int rows, int K, uint8_t* q, uint8_t* sf, cudaStream_t st);
+int b200_rope(void* x, int f32, int64_t st_t, int64_t st_h, int T, int H, int d, const int* pos, const float* table,
+              cudaStream_t st);
+int b200_kv_store(const void* kv, int f32, int64_t ld, int T, int L, int R, const float* w, float eps, const int* pos,
+                  const float* table, const int64_t* slots, uint8_t* cache, float kv_scale, cudaStream_t st);
+int b200_router(const float* logits, const float* bias, int T, int E, int G, int topk_group, int K, float scaling,
+                int renorm, float* w_out, int* id_out, cudaStream_t st);
+int b200_moe_align(const int* ids, const float* w, int T, int K, int first, int E, int* seg_start, int* seg_count,
+                   int* row_token, float* row_weight, int* pair_row, int* total_rows, cudaStream_t st);
+int b200_moe_gather(const uint8_t* xq, const uint8_t* xsf, const int* row_token, int rows_total, int Kd, uint8_t* dq,
+                    uint8_t* dsf, cudaStream_t st);
+int b200_moe_combine(const void* y, const int* pair_row, int T, int K, int D, const void* add, int add_f32, void* out,
+                     int out_f32, cudaStream_t st);

@@ -1,0 +1,201 @@
+// RMSNorm / residual-add / MXFP8 quantization kernels.
+//
+// One CTA per row; each thread owns 8 consecutive elements per pass (16-byte
+// loads), so 4 neighbouring lanes hold one 32-element scale block and the
+// block amax needs two shuffles.  Scales are written straight into the
+// sf128x4 layout the tcgen05 GEMM copies into TMEM.
+//
+// Reference parity: K5 `combine_norm_mxfp8` (hq_unit.cu:170), K8
+// `qnorm_mxfp8` (qn_unit.cu:192), K3/K4 MXFP8 quantizers (gq_unit.cu:140,222).
+#include "../common/ptx.cuh"
+#include "elementwise.h"
+
+namespace b200 {
+namespace ew {
+
+constexpr int kThreads = 256;
+
+__device__ __forceinline__ int64_t sf_off(int row, int kblock, int kb_total) {
+  const int rb = row >> 7, r = row & 127, kc = kblock >> 2, c = kblock & 3;
+  return ((int64_t)(rb * (kb_total >> 2) + kc) << 9) + ((r & 31) << 4) + ((r >> 5) << 2) + c;
+}
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&v)[8]);
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float (&v)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+__device__ __forceinline__ void store8_bf16(__nv_bfloat16* p, const float (&v)[8]) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+__device__ __forceinline__ void store8_f32(float* p, const float (&v)[8]) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+// Quantize 8 values held by this thread as part of a 32-block spread over 4
+// consecutive lanes; writes 8 e4m3 bytes and (lane % 4 == 0) the scale byte.
+__device__ __forceinline__ void quant8(const float (&v)[8], uint8_t* q, uint8_t* sf_base, int row, int col,
+                                       int kb_total, bool valid) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+  const int e = ceil_log2_bits(amax * (1.0f / 448.0f));
+  const float inv = exp2_int(-e);
+  uint2 out;
+  uint16_t* o16 = reinterpret_cast<uint16_t*>(&out);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) o16[i] = f2_to_e4m3x2(v[2 * i] * inv, v[2 * i + 1] * inv);
+  if (!valid) return;
+  *reinterpret_cast<uint2*>(q) = out;
+  if ((col & 31) == 0) sf_base[sf_off(row, col >> 5, kb_total)] = uint8_t(e + 127);
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float s = 0.f;
+  if (threadIdx.x < 32) {
+    s = (l < (int)(blockDim.x >> 5)) ? red[l] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (l == 0) red[0] = s;
+  }
+  __syncthreads();
+  return red[0];
+}
+
+// ---------------------------------------------------------------------------
+// x [rows, K] (+ optional residual add) -> rmsnorm -> {bf16 copy, mxfp8}
+//   MODE 0: y = rmsnorm(x)                       (x bf16 or fp32)
+//   MODE 1: r = r + x; y = rmsnorm(r)            (x bf16, r fp32 in place)
+// Outputs (each optional): y_bf16 [rows, K], q [rows, K] e4m3 + packed sf.
+// Rows longer than 256 * 8 * kMaxIt are not supported (K <= 16384).
+// ---------------------------------------------------------------------------
+constexpr int kMaxIt = 8;
+
+template <typename TX, int MODE>
+__global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const TX* __restrict__ x, int ldx, float* residual,
+                                                           const float* __restrict__ w, float eps, int K,
+                                                           __nv_bfloat16* y, int ldy, uint8_t* q, uint8_t* sf) {
+  __shared__ float red[32];
+  const int row = blockIdx.x;
+  pdl_wait();
+  const int units = K >> 3;
+  float v[kMaxIt][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int it = 0; it < kMaxIt; ++it) {
+    const int u = it * kThreads + threadIdx.x;
+    if (u < units) {
+      load8<TX>(x + (int64_t)row * ldx + u * 8, v[it]);
+      if (MODE == 1) {
+        float r[8];
+        float* rp = residual + (int64_t)row * K + u * 8;
+        load8<float>(rp, r);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[it][i] += r[i];
+        store8_f32(rp, v[it]);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += v[it][i] * v[it][i];
+    }
+  }
+  const float tot = block_sum(ss, red);
+  const float rs = rsqrtf(tot / float(K) + eps);
+  const int kb_total = K >> 5;
+#pragma unroll
+  for (int it = 0; it < kMaxIt; ++it) {
+    const int u = it * kThreads + threadIdx.x;
+    // all lanes of a warp take part in the shuffles of quant8
+    if (it * kThreads >= units) break;
+    float o[8];
+    if (u < units) {
+      const float4 w0 = *reinterpret_cast<const float4*>(w + u * 8);
+      const float4 w1 = *reinterpret_cast<const float4*>(w + u * 8 + 4);
+      const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = v[it][i] * rs * wv[i];
+      if (y) store8_bf16(y + (int64_t)row * ldy + u * 8, o);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = 0.f;
+    }
+    if (q) quant8(o, q + (int64_t)row * K + u * 8, sf, row, u * 8, kb_total, u < units);
+  }
+  pdl_launch_dependents();
+}
+
+// Plain MXFP8 quantization of x [rows, K] (bf16 or fp32).
+template <typename TX>
+__global__ void __launch_bounds__(kThreads) quant_kernel(const TX* __restrict__ x, int ldx, int K, uint8_t* q,
+                                                         uint8_t* sf) {
+  const int row = blockIdx.y;
+  const int u = blockIdx.x * kThreads + threadIdx.x;
+  const int units = K >> 3;
+  pdl_wait();
+  float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (u < units) load8<TX>(x + (int64_t)row * ldx + u * 8, v);
+  quant8(v, q + (int64_t)row * K + u * 8, sf, row, u * 8, K >> 5, u < units);
+  pdl_launch_dependents();
+}
+
+}  // namespace ew
+}  // namespace b200
+
+using namespace b200::ew;
+
+int b200_rmsnorm(const void* x, int x_is_f32, int ldx, float* residual, const float* w, float eps, int rows, int K,
+                 void* y, int ldy, uint8_t* q, uint8_t* sf, cudaStream_t st) {
+  if (K % 32 != 0 || K > kThreads * 8 * kMaxIt || rows <= 0) return -1;
+  dim3 grid(rows), block(kThreads);
+  __nv_bfloat16* yb = reinterpret_cast<__nv_bfloat16*>(y);
+  if (residual) {
+    rmsnorm_kernel<__nv_bfloat16, 1><<<grid, block, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx,
+                                                              residual, w, eps, K, yb, ldy, q, sf);
+  } else if (x_is_f32) {
+    rmsnorm_kernel<float, 0><<<grid, block, 0, st>>>(reinterpret_cast<const float*>(x), ldx, nullptr, w, eps, K,
+                                                      yb, ldy, q, sf);
+  } else {
+    rmsnorm_kernel<__nv_bfloat16, 0><<<grid, block, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx,
+                                                              nullptr, w, eps, K, yb, ldy, q, sf);
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : 1;
+}
+
+int b200_quant_mxfp8(const void* x, int x_is_f32, int ldx, int rows, int K, uint8_t* q, uint8_t* sf,
+                     cudaStream_t st) {
+  if (K % 128 != 0 || rows <= 0) return -1;
+  dim3 grid((K / 8 + kThreads - 1) / kThreads, rows), block(kThreads);
+  if (x_is_f32)
+    quant_kernel<float><<<grid, block, 0, st>>>(reinterpret_cast<const float*>(x), ldx, K, q, sf);
+  else
+    quant_kernel<__nv_bfloat16><<<grid, block, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, K, q, sf);
+  return cudaGetLastError() == cudaSuccess ? 0 : 1;
+}

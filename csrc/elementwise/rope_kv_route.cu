@@ -1,0 +1,328 @@
+// RoPE, latent-KV cache store, sigmoid group-limited router top-k, and the
+// MoE dispatch layout (expert segments, row gather, weighted combine).
+//
+// Reference parity: K9 `q_rope_fp8` (qr_unit.cu:104), K10 `inv_rope_tail`
+// (ro_unit.cu:73), K12 `route_e5_kernel` (route_e5.cu:853; here V3's sigmoid
+// + group-limited top-k instead of sqrtsoftplus + E5 prune) and the routing
+// record it writes for the expert GEMMs (rr.py:1-15).
+#include "../common/ptx.cuh"
+#include "elementwise.h"
+
+namespace b200 {
+namespace ew2 {
+
+__device__ __forceinline__ float ld_any(const void* p, int64_t i, int f32) {
+  return f32 ? reinterpret_cast<const float*>(p)[i] : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+}
+
+// In-place RoPE on x[t, h, 0:d] (interleaved pairs); table [P, d] = cos | sin.
+__global__ void rope_kernel(void* x, int f32, int64_t st_t, int64_t st_h, int H, int d, const int* pos,
+                            const float* table) {
+  const int t = blockIdx.x;
+  const int half = d >> 1;
+  pdl_wait();
+  const int p = pos[t];
+  for (int i = threadIdx.x; i < H * half; i += blockDim.x) {
+    const int h = i / half, j = i % half;
+    const int64_t base = (int64_t)t * st_t + (int64_t)h * st_h + 2 * j;
+    const float c = table[(int64_t)p * d + j], s = table[(int64_t)p * d + half + j];
+    if (f32) {
+      float* xp = reinterpret_cast<float*>(x);
+      const float a = xp[base], b = xp[base + 1];
+      xp[base] = a * c - b * s;
+      xp[base + 1] = a * s + b * c;
+    } else {
+      __nv_bfloat16* xp = reinterpret_cast<__nv_bfloat16*>(x);
+      const float a = __bfloat162float(xp[base]), b = __bfloat162float(xp[base + 1]);
+      xp[base] = __float2bfloat16(a * c - b * s);
+      xp[base + 1] = __float2bfloat16(a * s + b * c);
+    }
+  }
+  pdl_launch_dependents();
+}
+
+// One warp per token: latent = rmsnorm(kv[:L]) * w, pe = rope(kv[L:L+R]);
+// cache[slot] = e4m3([latent | pe] / kv_scale).  L % 32 == 0, R == 64.
+__global__ void kv_store_kernel(const void* kv, int f32, int64_t ld, int T, int L, int R, const float* w, float eps,
+                                const int* pos, const float* table, const int64_t* slots, uint8_t* cache,
+                                float inv_scale) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  pdl_wait();
+  if (warp >= T) return;
+  const int64_t row = (int64_t)warp * ld;
+  float ss = 0.f;
+  for (int i = lane; i < L; i += 32) {
+    const float v = ld_any(kv, row + i, f32);
+    ss += v * v;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float rs = rsqrtf(ss / float(L) + eps);
+  uint8_t* dst = cache + slots[warp] * (int64_t)(L + R);
+  for (int i = 2 * lane; i < L; i += 64) {
+    const float a = ld_any(kv, row + i, f32) * rs * w[i] * inv_scale;
+    const float b = ld_any(kv, row + i + 1, f32) * rs * w[i + 1] * inv_scale;
+    *reinterpret_cast<uint16_t*>(dst + i) = f2_to_e4m3x2(a, b);
+  }
+  const int p = pos[warp];
+  const int half = R >> 1;
+  for (int j = lane; j < half; j += 32) {
+    const float a = ld_any(kv, row + L + 2 * j, f32), b = ld_any(kv, row + L + 2 * j + 1, f32);
+    const float c = table[(int64_t)p * R + j], s = table[(int64_t)p * R + half + j];
+    *reinterpret_cast<uint16_t*>(dst + L + 2 * j) = f2_to_e4m3x2((a * c - b * s) * inv_scale,
+                                                                  (a * s + b * c) * inv_scale);
+  }
+  pdl_launch_dependents();
+}
+
+// Router: one warp per token over E <= 256 experts (E % 32 == 0).
+// scores = sigmoid(logits); choice = scores + bias; group score = sum of the
+// top-2 choices in each of G groups; keep the top `topk_group` groups; pick
+// the top-k choices among them; weights = scores renormalised * scaling.
+// Ties resolve to the lower expert index.
+constexpr int kMaxEPerLane = 8;
+
+__global__ void router_kernel(const float* logits, const float* bias, int T, int E, int G, int topk_group, int K,
+                              float scaling, int renorm, float* w_out, int* id_out) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  pdl_wait();
+  if (warp >= T) return;
+  const int per = E / 32;     // experts per lane, contiguous: lane owns [lane*per, lane*per+per)
+  float sc[kMaxEPerLane], ch[kMaxEPerLane];
+#pragma unroll
+  for (int i = 0; i < kMaxEPerLane; ++i) {
+    if (i < per) {
+      const int e = lane * per + i;
+      const float l = logits[(int64_t)warp * E + e];
+      sc[i] = 1.0f / (1.0f + __expf(-l));
+      ch[i] = sc[i] + bias[e];
+    } else {
+      sc[i] = 0.f;
+      ch[i] = -INFINITY;
+    }
+  }
+  // group selection: group g covers experts [g*E/G, (g+1)*E/G) = lanes [g*32/G, (g+1)*32/G)
+  if (G > 1) {
+    const int lanes_per_group = 32 / G;
+    float b1 = -INFINITY, b2 = -INFINITY;   // top-2 within this lane
+#pragma unroll
+    for (int i = 0; i < kMaxEPerLane; ++i) {
+      if (i < per) {
+        const float v = ch[i];
+        if (v > b1) { b2 = b1; b1 = v; } else if (v > b2) b2 = v;
+      }
+    }
+    // merge top-2 across the lanes of the group
+    for (int o = 1; o < lanes_per_group; o <<= 1) {
+      const float o1 = __shfl_xor_sync(0xffffffffu, b1, o);
+      const float o2 = __shfl_xor_sync(0xffffffffu, b2, o);
+      const float n1 = fmaxf(b1, o1);
+      const float n2 = fmaxf(fminf(b1, o1), fmaxf(b2, o2));
+      b1 = n1;
+      b2 = n2;
+    }
+    const float gscore = b1 + b2;            // same value on every lane of the group
+    const int my_group = lane / lanes_per_group;
+    // rank groups: group g is kept if fewer than topk_group groups beat it
+    int beat = 0;
+    for (int g = 0; g < G; ++g) {
+      const float og = __shfl_sync(0xffffffffu, gscore, g * lanes_per_group);
+      if (og > gscore || (og == gscore && g < my_group)) ++beat;
+    }
+    if (beat >= topk_group) {
+#pragma unroll
+      for (int i = 0; i < kMaxEPerLane; ++i) ch[i] = -INFINITY;
+    }
+  }
+  float wsum = 0.f;
+  float wk = 0.f;
+  int idk = 0;
+  for (int k = 0; k < K; ++k) {
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < kMaxEPerLane; ++i) {
+      if (i < per && ch[i] > best) { best = ch[i]; bi = lane * per + i; }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+    }
+    const int owner = bi / per;
+    float s = 0.f;
+    if (lane == owner) {
+      const int li = bi - lane * per;
+#pragma unroll
+      for (int i = 0; i < kMaxEPerLane; ++i)
+        if (i == li) { s = sc[i]; ch[i] = -INFINITY; }
+    }
+    s = __shfl_sync(0xffffffffu, s, owner);
+    wsum += s;
+    if (lane == k) { wk = s; idk = bi; }
+  }
+  if (lane < K) {
+    const float norm = (renorm && K > 1) ? 1.0f / (wsum + 1e-20f) : 1.0f;
+    w_out[(int64_t)warp * K + lane] = wk * norm * scaling;
+    id_out[(int64_t)warp * K + lane] = idk;
+  }
+  pdl_launch_dependents();
+}
+
+// ---------------------------------------------------------------------------
+// MoE dispatch layout for the local experts [first, first + E).
+//   seg_count[e]  rows routed to local expert e
+//   seg_start[e]  first sorted row of e (128-aligned)
+//   row_token[r]  token of sorted row r;  row_weight[r] its routing weight
+//   pair_row[t*K+j]  sorted row of (t, j), or -1 if the expert is not local
+// One CTA; counts via shared-memory atomics.
+// ---------------------------------------------------------------------------
+__global__ void moe_align_kernel(const int* ids, const float* w, int T, int K, int first, int E, int* seg_start,
+                                 int* seg_count, int* row_token, float* row_weight, int* pair_row, int* total_rows) {
+  extern __shared__ int sh[];
+  int* cnt = sh;          // [E]
+  int* start = sh + E;    // [E]
+  int* fill = sh + 2 * E; // [E]
+  pdl_wait();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) { cnt[e] = 0; fill[e] = 0; }
+  __syncthreads();
+  const int n = T * K;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int e = ids[i] - first;
+    if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int e = 0; e < E; ++e) {
+      start[e] = acc;
+      acc += (cnt[e] + 127) & ~127;
+    }
+    *total_rows = acc;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    seg_start[e] = start[e];
+    seg_count[e] = cnt[e];
+  }
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int e = ids[i] - first;
+    if (e >= 0 && e < E) {
+      const int r = start[e] + atomicAdd(&fill[e], 1);
+      row_token[r] = i / K;
+      row_weight[r] = w[i];
+      pair_row[i] = r;
+    } else {
+      pair_row[i] = -1;
+    }
+  }
+  pdl_launch_dependents();
+}
+
+// Gather MXFP8 rows: dst row r <- src row row_token[r] (data + scale bytes).
+// grid (rows_total), block 128.  Rows not in any segment are skipped via
+// row_token < 0 (the caller initialises row_token to -1).
+__global__ void moe_gather_kernel(const uint8_t* xq, const uint8_t* xsf, const int* row_token, int rows_total, int Kd,
+                                  uint8_t* dq, uint8_t* dsf) {
+  const int r = blockIdx.x;
+  pdl_wait();
+  if (r >= rows_total) return;
+  const int t = row_token[r];
+  if (t < 0) return;
+  const uint4* s = reinterpret_cast<const uint4*>(xq + (int64_t)t * Kd);
+  uint4* d = reinterpret_cast<uint4*>(dq + (int64_t)r * Kd);
+  for (int i = threadIdx.x; i < Kd / 16; i += blockDim.x) d[i] = s[i];
+  const int kb = Kd / 32;
+  for (int b = threadIdx.x; b < kb; b += blockDim.x) {
+    const int64_t so = ((int64_t)((t >> 7) * (kb >> 2) + (b >> 2)) << 9) + ((t & 31) << 4) + (((t & 127) >> 5) << 2) + (b & 3);
+    const int64_t doff = ((int64_t)((r >> 7) * (kb >> 2) + (b >> 2)) << 9) + ((r & 31) << 4) + (((r & 127) >> 5) << 2) + (b & 3);
+    dsf[doff] = xsf[so];
+  }
+  pdl_launch_dependents();
+}
+
+// out[t, :] = sum_j y[pair_row[t*K+j], :] (+ add[t, :]) in fp32 -> bf16 / f32.
+__global__ void moe_combine_kernel(const __nv_bfloat16* y, const int* pair_row, int T, int K, int D, const void* add,
+                                   int add_f32, void* out, int out_f32) {
+  const int t = blockIdx.x;
+  pdl_wait();
+  for (int c = threadIdx.x * 2; c < D; c += blockDim.x * 2) {
+    float a0 = 0.f, a1 = 0.f;
+    for (int j = 0; j < K; ++j) {
+      const int r = pair_row[t * K + j];
+      if (r >= 0) {
+        const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(y + (int64_t)r * D + c));
+        a0 += v.x;
+        a1 += v.y;
+      }
+    }
+    if (add) {
+      a0 += ld_any(add, (int64_t)t * D + c, add_f32);
+      a1 += ld_any(add, (int64_t)t * D + c + 1, add_f32);
+    }
+    if (out_f32) {
+      reinterpret_cast<float*>(out)[(int64_t)t * D + c] = a0;
+      reinterpret_cast<float*>(out)[(int64_t)t * D + c + 1] = a1;
+    } else {
+      *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<__nv_bfloat16*>(out) + (int64_t)t * D + c) =
+          __floats2bfloat162_rn(a0, a1);
+    }
+  }
+  pdl_launch_dependents();
+}
+
+}  // namespace ew2
+}  // namespace b200
+
+using namespace b200::ew2;
+
+int b200_rope(void* x, int f32, int64_t st_t, int64_t st_h, int T, int H, int d, const int* pos, const float* table,
+              cudaStream_t st) {
+  if (T <= 0) return 0;
+  rope_kernel<<<T, 128, 0, st>>>(x, f32, st_t, st_h, H, d, pos, table);
+  return cudaGetLastError() == cudaSuccess ? 0 : 1;
+}
+
+int b200_kv_store(const void* kv, int f32, int64_t ld, int T, int L, int R, const float* w, float eps, const int* pos,
+                  const float* table, const int64_t* slots, uint8_t* cache, float kv_scale, cudaStream_t st) {
+  if (T <= 0) return 0;
+  if (L % 64 != 0) return -1;
+  const int threads = 128;
+  const int blocks = (T * 32 + threads - 1) / threads;
+  kv_store_kernel<<<blocks, threads, 0, st>>>(kv, f32, ld, T, L, R, w, eps, pos, table, slots, cache, 1.0f / kv_scale);
+  return cudaGetLastError() == cudaSuccess ? 0 : 1;
+}
+
+int b200_router(const float* logits, const float* bias, int T, int E, int G, int topk_group, int K, float scaling,
+                int renorm, float* w_out, int* id_out, cudaStream_t st) {
+  if (T <= 0) return 0;
+  if (E % 32 != 0 || E / 32 > kMaxEPerLane || K > 32 || (G > 1 && (32 % G != 0))) return -1;
+  const int threads = 128;
+  router_kernel<<<(T * 32 + threads - 1) / threads, threads, 0, st>>>(logits, bias, T, E, G, topk_group, K, scaling,
+                                                                       renorm, w_out, id_out);
+  return cudaGetLastError() == cudaSuccess ? 0 : 1;
+}
+
+int b200_moe_align(const int* ids, const float* w, int T, int K, int first, int E, int* seg_start, int* seg_count,
+                   int* row_token, float* row_weight, int* pair_row, int* total_rows, cudaStream_t st) {
+  moe_align_kernel<<<1, 1024, 3 * E * sizeof(int), st>>>(ids, w, T, K, first, E, seg_start, seg_count, row_token,
+                                                         row_weight, pair_row, total_rows);
+  return cudaGetLastError() == cudaSuccess ? 0 : 1;
+}
+
+int b200_moe_gather(const uint8_t* xq, const uint8_t* xsf, const int* row_token, int rows_total, int Kd, uint8_t* dq,
+                    uint8_t* dsf, cudaStream_t st) {
+  if (rows_total <= 0) return 0;
+  moe_gather_kernel<<<rows_total, 128, 0, st>>>(xq, xsf, row_token, rows_total, Kd, dq, dsf);
+  return cudaGetLastError() == cudaSuccess ? 0 : 1;
+}
+
+int b200_moe_combine(const void* y, const int* pair_row, int T, int K, int D, const void* add, int add_f32, void* out,
+                     int out_f32, cudaStream_t st) {
+  if (T <= 0) return 0;
+  moe_combine_kernel<<<T, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(y), pair_row, T, K, D, add, add_f32,
+                                        out, out_f32);
+  return cudaGetLastError() == cudaSuccess ? 0 : 1;
+}

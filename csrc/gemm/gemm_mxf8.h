@@ -1,0 +1,41 @@
+// Host interface of the MXFP8 tcgen05 GEMM (see gemm_mxf8.cu).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+enum GemmEpi : int {
+  kEpiStoreBf16 = 0,     // out[row, n] = bf16(acc)
+  kEpiAtomicF32 = 1,     // out[row, n] += acc (fp32, split-K)
+  kEpiSwiglu = 2,        // q_out/sf_out = mxfp8(silu(gate) * up)
+  kEpiWeightedBf16 = 3,  // out[row, n] = bf16(acc * row_weight[row])  (grouped only)
+};
+
+struct GemmArgs {
+  const uint8_t* w;        // e4m3 weights [E *] nw x k
+  const uint8_t* w_sf;     // packed sf128x4 scales of w
+  int64_t w_sf_estride;    // bytes between experts' scales (grouped)
+  const uint8_t* x;        // e4m3 activations [x_rows, k]
+  const uint8_t* x_sf;     // packed scales of x
+  int64_t x_rows;          // rows addressable in x (for the TMA bounds)
+  int nw;                  // weight rows per expert (dense: total rows)
+  int nw_total;            // dense: rows of w
+  int t;                   // dense: tokens
+  int k;
+  int splits;              // dense split-K factor (kEpiAtomicF32)
+  int num_experts;         // > 0: grouped mode
+  const int* seg_start;    // grouped: first sorted row per expert (128-aligned)
+  const int* seg_count;    // grouped: rows per expert
+  int max_rows_per_expert; // grouped: upper bound of seg_count (grid size)
+  int epi;
+  void* out;
+  int ldo;
+  uint8_t* q_out;
+  uint8_t* sf_out;
+  int ldq;
+  int inter;
+  const float* row_weight;
+  uint32_t* err;
+  int pdl;
+};
+
+int b200_gemm_mxf8(const GemmArgs* args, cudaStream_t stream);

@@ -1,0 +1,200 @@
+"""Numerics of the sm_100a kernels against plain-PyTorch fp32 references."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+@pytest.fixture(autouse=True)
+def _native():
+    from b200ds import ops
+    ops.set_impl("native")
+    import b200ds._C  # noqa: F401  (loud failure if the extension is missing)
+
+
+def rel_err(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / (b.norm() + 1e-12)).item()
+
+
+@pytest.mark.parametrize("T,K", [(1, 128), (7, 512), (130, 7168), (64, 1536)])
+def test_quant_matches_reference(T, K):
+    from b200ds.ops import cuda
+    from b200ds.ops.quant import quant_mxfp8_ref
+    g = torch.Generator(device=DEV).manual_seed(0)
+    x = torch.randn(T, K, device=DEV, generator=g).to(torch.bfloat16) * 3
+    a = cuda.quant(x)
+    q, sf = quant_mxfp8_ref(x.float())
+    n = q.numel()
+    assert torch.equal(a.q.view(torch.uint8), q.view(torch.uint8))
+    assert torch.equal(a.sf[: sf.numel()].view(-1)[: sf.numel()], sf) or \
+        torch.equal(_valid_sf(a.sf, T, K), _valid_sf(sf, T, K))
+
+
+def _valid_sf(sf, T, K):
+    from b200ds.ops.quant import unpack_sf
+    return unpack_sf(sf, T, K)
+
+
+@pytest.mark.parametrize("T,K", [(3, 7168), (64, 1536), (257, 512)])
+def test_rmsnorm_quant(T, K):
+    from b200ds.ops import cuda, ref
+    from b200ds.ops.quant import quant_mxfp8_ref, unpack_sf
+    x = torch.randn(T, K, device=DEV).to(torch.bfloat16)
+    w = torch.rand(K, device=DEV) + 0.5
+    a = cuda.rmsnorm_quant(x, w, 1e-6)
+    y = ref.rmsnorm(x, w, 1e-6)
+    assert rel_err(a.hf, y) < 4e-3
+    # dequantized output close to the fp32 normalized value
+    from b200ds.ops.quant import dequant_mxfp8
+    assert rel_err(dequant_mxfp8(a.q, a.sf), y) < 4e-2
+
+
+def test_add_rmsnorm_residual():
+    from b200ds.ops import cuda, ref
+    T, K = 33, 7168
+    a = torch.randn(T, K, device=DEV).to(torch.bfloat16)
+    r = torch.randn(T, K, device=DEV)
+    w = torch.rand(K, device=DEV) + 0.5
+    r0 = r.clone()
+    y, r2 = cuda.add_rmsnorm_act(a, r, w, 1e-6, None)
+    exp_r = r0 + a.float()
+    assert torch.allclose(r2, exp_r, atol=1e-5)
+    assert rel_err(y, ref.rmsnorm(exp_r, w, 1e-6)) < 4e-3
+
+
+def _mx(x):
+    from b200ds.ops.quant import quant_mxfp8_ref, MXFP8Tensor
+    q, sf = quant_mxfp8_ref(x.float())
+    return MXFP8Tensor(q, sf)
+
+
+@pytest.mark.parametrize("T,N,K", [(1, 256, 256), (5, 384, 1024), (16, 128, 7168), (40, 512, 2048),
+                                   (64, 2176, 7168), (130, 256, 512), (300, 384, 1024)])
+def test_gemm_mxf8(T, N, K):
+    from b200ds.ops import QAct, cuda, ref
+    x = torch.randn(T, K, device=DEV)
+    w = torch.randn(N, K, device=DEV) * 0.05
+    a = _mx(x)
+    wq = _mx(w)
+    exp = ref.gemm_mxfp8(a.data, a.sf, wq.data, wq.sf)
+    got = cuda.gemm(QAct(a.data, a.sf), wq, torch.bfloat16)
+    assert got.shape == (T, N)
+    assert rel_err(got, exp) < 5e-3, rel_err(got, exp)
+
+
+def test_gemm_splitk_fp32():
+    from b200ds.ops import QAct, cuda, ref
+    T, N, K = 8, 256, 7168
+    a = _mx(torch.randn(T, K, device=DEV))
+    wq = _mx(torch.randn(N, K, device=DEV) * 0.05)
+    out = torch.zeros(T, N, device=DEV)
+    cuda._gemm_raw(QAct(a.data, a.sf), wq, out, 1, splits=4)
+    exp = ref.gemm_mxfp8(a.data, a.sf, wq.data, wq.sf)
+    assert rel_err(out, exp) < 1e-4
+
+
+@pytest.mark.parametrize("T", [1, 20, 64, 200])
+def test_gemm_swiglu_quant(T):
+    from b200ds.ops import QAct, cuda, ref
+    from b200ds.ops.quant import dequant_mxfp8
+    K, I = 1024, 256
+    a = _mx(torch.randn(T, K, device=DEV))
+    wq = _mx(torch.randn(2 * I, K, device=DEV) * 0.05)
+    o = cuda.gemm_swiglu_quant(QAct(a.data, a.sf), wq)
+    y = ref.swiglu(ref.gemm_mxfp8(a.data, a.sf, wq.data, wq.sf))
+    assert rel_err(dequant_mxfp8(o.q, o.sf)[:T], y) < 4e-2
+
+
+def test_rope_and_kv_store():
+    from b200ds.config import small_gpu_config
+    from b200ds.models.rope import cos_sin_table
+    from b200ds.ops import cuda, ref
+    cfg = small_gpu_config()
+    tab = cos_sin_table(cfg, 4096, device=DEV)
+    T, H = 9, 16
+    pos = torch.randint(0, 4000, (T,), device=DEV, dtype=torch.int32)
+    q = torch.randn(T, H, 192, device=DEV).to(torch.bfloat16)
+    exp = ref.rope(q[..., 128:], pos, tab)
+    cuda.rope(q[..., 128:], pos, tab)
+    assert rel_err(q[..., 128:], exp) < 1e-2
+    kv = torch.randn(T, 576, device=DEV).to(torch.bfloat16)
+    w = torch.rand(512, device=DEV) + 0.5
+    cache = torch.zeros(64, 576, dtype=torch.float8_e4m3fn, device=DEV)
+    slots = torch.randperm(64, device=DEV)[:T].long()
+    cuda.kv_store(kv, w, 1e-6, tab, pos, cache, slots, 0.5, 512)
+    ckv = ref.rmsnorm(kv[:, :512], w, 1e-6)
+    kpe = ref.rope(kv[:, 512:], pos, tab)
+    exp = ref.kv_quant(ckv, kpe, 0.5)
+    got = cache[slots]
+    assert rel_err(got.float(), exp.float()) < 3e-2
+
+
+@pytest.mark.parametrize("E,G,TG,K", [(256, 8, 4, 8), (32, 4, 2, 8), (64, 1, 1, 6)])
+def test_router(E, G, TG, K):
+    from b200ds.ops import ref
+    from b200ds import _C
+    T = 50
+    logits = torch.randn(T, E, device=DEV)
+    bias = torch.randn(E, device=DEV) * 0.1
+    w = torch.empty(T, K, device=DEV)
+    ids = torch.empty(T, K, dtype=torch.int32, device=DEV)
+    _C.router(logits, bias, G, TG, K, 2.5, True, w, ids)
+    ew, eids = ref.router_topk(logits, bias, K, G, TG, 2.5, True)
+    for t in range(T):
+        assert set(ids[t].tolist()) == set(eids[t].tolist())
+        m = {int(i): float(x) for i, x in zip(ids[t], w[t])}
+        for i, x in zip(eids[t].tolist(), ew[t].tolist()):
+            assert abs(m[i] - x) < 1e-4
+
+
+def test_moe_experts_grouped():
+    from b200ds.ops import ExpertWeights, QAct, cuda, ref
+    from b200ds.ops.quant import MXFP8Tensor, quant_mxfp8_ref
+    import b200ds.ops as ops
+    T, H, I, E, K = 37, 1024, 256, 16, 4
+    first = 8          # this rank owns experts 8..23 of 32
+    w13 = [_mx(torch.randn(2 * I, H, device=DEV) * 0.05) for _ in range(E)]
+    w2 = [_mx(torch.randn(H, I, device=DEV) * 0.05) for _ in range(E)]
+    ex = ExpertWeights(first, E, MXFP8Tensor(torch.stack([w.data for w in w13]), torch.stack([w.sf for w in w13])),
+                       MXFP8Tensor(torch.stack([w.data for w in w2]), torch.stack([w.sf for w in w2])), I)
+    x = torch.randn(T, H, device=DEV)
+    a = _mx(x)
+    ids = torch.stack([torch.randperm(32, device=DEV)[:K] for _ in range(T)]).int()
+    wts = torch.rand(T, K, device=DEV)
+    got = cuda.moe_experts(QAct(a.data, a.sf), wts, ids, ex, torch.float32)
+    # reference: same math on the CPU path
+    exc = ExpertWeights(first, E, MXFP8Tensor(ex.w13.data.cpu(), ex.w13.sf.cpu()),
+                        MXFP8Tensor(ex.w2.data.cpu(), ex.w2.sf.cpu()), I)
+    from b200ds.ops.quant import dequant_mxfp8
+    exp = ops.moe_experts(dequant_mxfp8(a.data, a.sf).cpu(), wts.cpu(), ids.cpu(), exc, torch.float32)
+    assert rel_err(got.cpu(), exp) < 3e-2, rel_err(got.cpu(), exp)
+
+
+def test_mla_simt_matches_reference():
+    from types import SimpleNamespace
+    from b200ds.ops import cuda, ref
+    B, H, L, R, ps = 3, 16, 512, 64, 16
+    lens = [5, 40, 77]
+    pages_per = [(n + ps - 1) // ps for n in lens]
+    bt = torch.zeros(B, max(pages_per), dtype=torch.int32)
+    nxt = 1
+    for b in range(B):
+        for j in range(pages_per[b]):
+            bt[b, j] = nxt
+            nxt += 1
+    cache = (torch.randn(nxt * ps, L + R) * 0.5).to(torch.float8_e4m3fn)
+    # queries: decode for b=0,1 and 3 prefill tokens of b=2
+    q_seq = torch.tensor([0, 1, 2, 2, 2], dtype=torch.int32)
+    q_pos = torch.tensor([4, 39, 74, 75, 76], dtype=torch.int32)
+    T = 5
+    q_abs = torch.randn(T, H, L).to(torch.bfloat16)
+    q_pe = torch.randn(T, H, R).to(torch.bfloat16)
+    fb = SimpleNamespace(block_table=bt.to(DEV), q_seq=q_seq.to(DEV), positions=q_pos.to(DEV))
+    got = cuda.mla_attention(q_abs.to(DEV), q_pe.to(DEV), cache.to(DEV), 0.7, fb, 0.06, ps)
+    exp = ref.mla_attention(q_abs, q_pe, cache, 0.7, bt, torch.tensor(lens), q_seq, q_pos, 0.06, ps)
+    assert rel_err(got.cpu(), exp) < 1e-2
