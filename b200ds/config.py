@@ -184,6 +184,7 @@ class EngineConfig:
     ep_size: int = 1                 # expert parallel width
     dp_attention: bool = False       # data-parallel attention (tp_size=1 per DP rank) + EP MoE
     page_size: int = 64              # tokens per KV page
+    max_model_len: int = 16384       # longest sequence (sizes graph block tables)
     max_num_seqs: int = 256          # concurrent running requests
     max_prefill_tokens: int = 16384  # chunked-prefill budget per step
     kv_cache_fraction: float = 0.85  # of free HBM after weights

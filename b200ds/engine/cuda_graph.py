@@ -1,0 +1,143 @@
+"""CUDA-graph capture and replay of the decode step, one graph per padded
+batch size.
+
+Static device buffers hold the step's metadata (token ids, positions, KV
+slots, block table, sequence lengths).  Each replay: the host fills pinned
+staging buffers, one async copy per buffer moves them to the device, the
+graph replays the whole forward (all layers, collectives included) plus
+greedy argmax, and the sampled ids come back to the host.  Padded rows use
+the reserved scratch page 0 so they never touch live KV.
+
+Reference parity: decode/verify forwards are captured by SGLang's graph
+runner (absent); the reference adds per-bucket eager graphs (fg.py, ag.py).
+"""
+from __future__ import annotations
+
+from typing import Dict, List, Optional
+
+import torch
+
+from ..models.batch import ForwardBatch
+
+
+class _Graph:
+    pass
+
+
+class DecodeGraphRunner:
+    def __init__(self, engine, batch_sizes=None, max_pages: Optional[int] = None):
+        self.eng = engine
+        self.model = engine.model
+        self.dev = engine.device
+        ecfg = engine.ecfg
+        self.page_size = ecfg.page_size
+        self.batch_sizes = sorted(batch_sizes or [b for b in ecfg.graph_batch_sizes if b <= ecfg.max_num_seqs])
+        if not self.batch_sizes or self.batch_sizes[-1] < ecfg.max_num_seqs:
+            self.batch_sizes.append(ecfg.max_num_seqs)
+        self.max_pages = max_pages or (ecfg.max_model_len + self.page_size - 1) // self.page_size
+        self.graphs: Dict[int, _Graph] = {}
+        self.pool = None
+        self.enabled = True
+
+    def can_run(self, n: int) -> bool:
+        return self.enabled and n <= self.batch_sizes[-1]
+
+    def _bucket(self, n: int) -> int:
+        for b in self.batch_sizes:
+            if b >= n:
+                return b
+        raise ValueError(n)
+
+    def _make_static(self, bs: int) -> _Graph:
+        g = _Graph()
+        d = self.dev
+        g.bs = bs
+        g.ids = torch.zeros(bs, dtype=torch.int32, device=d)
+        g.pos = torch.zeros(bs, dtype=torch.int32, device=d)
+        g.q_seq = torch.arange(bs, dtype=torch.int32, device=d)
+        g.slots = torch.zeros(bs, dtype=torch.int64, device=d)
+        g.lens = torch.ones(bs, dtype=torch.int32, device=d)
+        g.bt = torch.zeros(bs, self.max_pages, dtype=torch.int32, device=d)
+        g.last = torch.arange(bs, dtype=torch.int64, device=d)
+        # pinned host staging
+        g.h_ids = torch.zeros(bs, dtype=torch.int32).pin_memory()
+        g.h_pos = torch.zeros(bs, dtype=torch.int32).pin_memory()
+        g.h_slots = torch.zeros(bs, dtype=torch.int64).pin_memory()
+        g.h_lens = torch.ones(bs, dtype=torch.int32).pin_memory()
+        g.h_bt = torch.zeros(bs, self.max_pages, dtype=torch.int32).pin_memory()
+        g.h_tok = torch.zeros(bs, dtype=torch.int64).pin_memory()
+        g.fb = ForwardBatch(input_ids=g.ids, positions=g.pos, q_seq=g.q_seq, out_slots=g.slots, seq_lens=g.lens,
+                            block_table=g.bt, last_idx=g.last, is_decode=True, max_q_len=1,
+                            max_seq_len=self.max_pages * self.page_size)
+        return g
+
+    def capture(self, bs: int) -> _Graph:
+        g = self._make_static(bs)
+        s = torch.cuda.Stream(device=self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                logits = self.model.forward(g.fb)
+                torch.argmax(logits, -1)
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        torch.cuda.synchronize(self.dev)
+        # keep_graph: the raw graph stays queryable (kernel-node census)
+        g.graph = torch.cuda.CUDAGraph(keep_graph=True)
+        if self.pool is None:
+            self.pool = torch.cuda.graph_pool_handle()
+        with torch.cuda.graph(g.graph, pool=self.pool):
+            g.logits = self.model.forward(g.fb)
+            g.tokens = torch.argmax(g.logits, -1)
+        g.graph.instantiate()
+        self.graphs[bs] = g
+        return g
+
+    def capture_all(self) -> None:
+        for bs in reversed(self.batch_sizes):
+            if bs not in self.graphs:
+                self.capture(bs)
+
+    def stage(self, g: _Graph, seqs: List[dict]) -> None:
+        """Fill the pinned staging buffers for this step and copy them."""
+        n = len(seqs)
+        ps = self.page_size
+        g.h_ids.zero_()
+        g.h_pos.zero_()
+        g.h_slots.zero_()
+        g.h_lens.fill_(1)
+        g.h_bt.zero_()
+        ids, pos, slots, lens = g.h_ids.numpy(), g.h_pos.numpy(), g.h_slots.numpy(), g.h_lens.numpy()
+        bt = g.h_bt.numpy()
+        for i, s in enumerate(seqs):
+            p = s["start"]
+            if len(s["pages"]) > self.max_pages:
+                raise ValueError("sequence longer than EngineConfig.max_model_len")
+            ids[i] = s["tokens"][0]
+            pos[i] = p
+            pages = s["pages"]
+            slots[i] = pages[p // ps] * ps + p % ps
+            lens[i] = p + 1
+            bt[i, : len(pages)] = pages
+        g.ids.copy_(g.h_ids, non_blocking=True)
+        g.pos.copy_(g.h_pos, non_blocking=True)
+        g.slots.copy_(g.h_slots, non_blocking=True)
+        g.lens.copy_(g.h_lens, non_blocking=True)
+        g.bt.copy_(g.h_bt, non_blocking=True)
+
+    def run(self, step, seqs: List[dict]) -> List[int]:
+        n = len(seqs)
+        bs = self._bucket(n)
+        g = self.graphs.get(bs) or self.capture(bs)
+        self.stage(g, seqs)
+        g.graph.replay()
+        greedy = all(r.params.temperature <= 0 for r in step.reqs)
+        if greedy:
+            g.h_tok.copy_(g.tokens, non_blocking=True)
+            torch.cuda.current_stream(self.dev).synchronize()
+            return g.h_tok[:n].tolist()
+        return self.eng._sample(step, g.logits[:n])
+
+    def release(self) -> None:
+        """Drop the graphs (before destroying the process group)."""
+        self.graphs.clear()
+        self.pool = None

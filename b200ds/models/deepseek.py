@@ -178,7 +178,7 @@ class DeepseekModel:
             return lw.ffn.down(a, out_dtype=out_dt)
         mw: MoEWeights = lw.ffn
         w, ids = ops.router(h, mw.gate, mw.bias, c)
-        out = ops.moe_experts(h, w, ids, mw.experts, out_dtype=out_dt)
+        out = ops.moe_experts(h, w, ids, mw.experts, out_dtype=out_dt, n_experts_total=c.n_routed_experts)
         if mw.shared_gate_up is not None:
             s = lw.ffn.shared_down(ops.gate_up_swiglu(h, mw.shared_gate_up), out_dtype=out_dt)
             out = out + s

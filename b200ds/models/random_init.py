@@ -1,10 +1,155 @@
-"""Random-init weights generated directly on the device, per rank."""
+"""Random-init weights generated directly on the device, per rank, in the
+serving formats (for benchmarks of the full-size architectures, whose fp32
+state dict would not fit in host memory).
+
+MXFP8 tensors get uniformly random e4m3 codes with the exponent MSB cleared
+(finite, |x| <= 1.875, RMS ~0.59) and a constant UE8M0 scale of 2^-5, i.e.
+weights with RMS ~0.018; bf16 tensors are N(0, 0.02); norms are ones; the
+router gate is N(0, 0.02) so expert load is near uniform.
+
+When the routed experts of all MoE layers do not fit in HBM (the 671B model
+on fewer than 8 GPUs), `weight_sets` distinct expert sets are generated and
+MoE layer i uses set i % weight_sets.  Every layer still streams its full
+expert weights from HBM (one layer's experts are far larger than L2), so the
+per-step work is that of the full model.
+"""
 from __future__ import annotations
 
+import math
+from typing import List, Optional
 
-def should_generate_on_device(cfg, device) -> bool:
-    return False
+import torch
+
+from ..config import EngineConfig, ModelConfig
+from ..ops import ExpertWeights
+from ..ops.quant import MXFP8Tensor, round_up
+from ..parallel.state import ParallelState
+from .deepseek import AttnWeights, DeepseekModel, DenseWeights, LayerWeights, Linear, MoEWeights
+
+SCALE_BYTE = 127 - 5
 
 
-def build_random_model(cfg, ecfg, ps, device, seed):
-    raise NotImplementedError
+def should_generate_on_device(cfg: ModelConfig, device) -> bool:
+    return torch.device(device).type == "cuda" and cfg.num_params() > 1_000_000_000
+
+
+class _Seeder:
+    def __init__(self, seed: int):
+        self.s = seed * 1_000_003 + 17
+
+    def next(self) -> int:
+        self.s += 1
+        return self.s
+
+
+def rand_mx(shape_lead, N: int, K: int, dev, seeder: _Seeder) -> MXFP8Tensor:
+    from .. import _C
+    Np = round_up(N, 128)
+    data = torch.empty(*shape_lead, Np, K, dtype=torch.uint8, device=dev)
+    _C.fill_bytes(data, seeder.next(), 0xBF, 0)
+    if Np != N:
+        data[..., N:, :] = 0
+    sf = torch.full((*shape_lead, Np * K // 32), SCALE_BYTE, dtype=torch.uint8, device=dev)
+    return MXFP8Tensor(data.view(torch.float8_e4m3fn), sf)
+
+
+def rand_bf16(shape, dev, gen, std=0.02, dtype=torch.bfloat16):
+    t = torch.empty(shape, dtype=dtype, device=dev)
+    t.normal_(0.0, std, generator=gen)
+    return t
+
+
+def expert_bytes_per_layer(cfg: ModelConfig, ep: int) -> int:
+    per = cfg.n_routed_experts // ep
+    h, I = cfg.hidden_size, cfg.moe_intermediate_size
+    return per * (2 * I * h + h * I) * (1 + 1 / 32)
+
+
+def auto_weight_sets(cfg: ModelConfig, ps: ParallelState, reserve_bytes: float, dev) -> int:
+    n_moe = sum(1 for i in range(cfg.num_hidden_layers) if cfg.is_moe_layer(i))
+    if n_moe == 0:
+        return 1
+    free, _ = torch.cuda.mem_get_info(dev)
+    per = expert_bytes_per_layer(cfg, ps.ep_size)
+    sets = int((free - reserve_bytes) // per)
+    return max(1, min(n_moe, sets))
+
+
+def build_random_model(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState, device, seed: int = 0,
+                       reserve_bytes: Optional[float] = None) -> DeepseekModel:
+    dev = torch.device(device)
+    gen = torch.Generator(device=dev).manual_seed(seed + 7919 * ps.rank)
+    sd = _Seeder(seed * 131 + ps.rank)
+    attn_tp = 1 if ecfg.dp_attention else ps.tp_size
+    tp = ps.tp_size
+    H = cfg.num_attention_heads
+    Hl = H // attn_tp
+    h = cfg.hidden_size
+    n_moe = sum(1 for i in range(cfg.num_hidden_layers) if cfg.is_moe_layer(i))
+    ones = lambda n: torch.ones(n, dtype=torch.float32, device=dev)
+
+    layers: List[LayerWeights] = []
+    # attention + dense + shared weights first (distinct per layer)
+    attn_list, dense_list, shared_list = [], [], []
+    for i in range(cfg.num_hidden_layers):
+        qkv_a = Linear(rand_mx((), cfg.q_lora_rank + cfg.kv_cache_dim, h, dev, sd))
+        q_b = Linear(rand_mx((), Hl * cfg.qk_head_dim, cfg.q_lora_rank, dev, sd))
+        o = Linear(rand_mx((), h, Hl * cfg.v_head_dim, dev, sd))
+        w_uk = rand_bf16((Hl, cfg.qk_nope_head_dim, cfg.kv_lora_rank), dev, gen)
+        w_uv = rand_bf16((Hl, cfg.v_head_dim, cfg.kv_lora_rank), dev, gen)
+        aw = AttnWeights(qkv_a=qkv_a, q_a_ln=ones(cfg.q_lora_rank), kv_a_ln=ones(cfg.kv_lora_rank), q_b=q_b,
+                         w_uk=w_uk, w_uv=w_uv, o_proj=o)
+        if cfg.index_n_heads:
+            aw.ix_wq_b = Linear(rand_bf16((cfg.index_n_heads * cfg.index_head_dim, cfg.q_lora_rank), dev, gen))
+            aw.ix_wk = rand_bf16((cfg.index_head_dim, h), dev, gen)
+            aw.ix_k_norm_w = ones(cfg.index_head_dim)
+            aw.ix_k_norm_b = torch.zeros(cfg.index_head_dim, device=dev)
+            aw.ix_weights = rand_bf16((cfg.index_n_heads, h), dev, gen)
+        attn_list.append(aw)
+        if cfg.is_moe_layer(i):
+            dense_list.append(None)
+            if cfg.n_shared_experts:
+                si = cfg.moe_intermediate_size * cfg.n_shared_experts // tp
+                shared_list.append((Linear(_gate_up(si, h, dev, sd)), Linear(rand_mx((), h, si, dev, sd))))
+            else:
+                shared_list.append((None, None))
+        else:
+            I = cfg.intermediate_size // tp
+            dense_list.append(DenseWeights(gate_up=Linear(_gate_up(I, h, dev, sd)), down=Linear(rand_mx((), h, I, dev, sd))))
+            shared_list.append((None, None))
+    embed = rand_bf16((cfg.vocab_size, h), dev, gen)
+    head = rand_bf16((cfg.vocab_size // tp if cfg.vocab_size % tp == 0 else -(-cfg.vocab_size // tp), h), dev, gen)
+
+    # routed experts: distinct sets as memory allows
+    per = cfg.n_routed_experts // ps.ep_size
+    first = ps.ep_rank * per
+    I = cfg.moe_intermediate_size
+    if reserve_bytes is None:
+        kv_tokens = ecfg.max_num_seqs * 4096
+        reserve_bytes = 24e9 + kv_tokens * cfg.kv_cache_dim * cfg.num_hidden_layers
+    sets = ecfg.weight_sets if ecfg.weight_sets > 0 else auto_weight_sets(cfg, ps, reserve_bytes, dev)
+    expert_sets = []
+    for s in range(min(sets, n_moe)):
+        w13 = rand_mx((per,), 2 * I, h, dev, sd)
+        w2 = rand_mx((per,), h, I, dev, sd)
+        expert_sets.append(ExpertWeights(first=first, count=per, w13=w13, w2=w2, inter=I))
+    moe_idx = 0
+    for i in range(cfg.num_hidden_layers):
+        if cfg.is_moe_layer(i):
+            gate = rand_bf16((cfg.n_routed_experts, h), dev, gen, dtype=torch.float32)
+            sgu, sdn = shared_list[i]
+            ffn = MoEWeights(gate=gate, bias=torch.zeros(cfg.n_routed_experts, device=dev),
+                             experts=expert_sets[moe_idx % len(expert_sets)], shared_gate_up=sgu, shared_down=sdn)
+            moe_idx += 1
+        else:
+            ffn = dense_list[i]
+        layers.append(LayerWeights(in_ln=ones(h), post_ln=ones(h), attn=attn_list[i], ffn=ffn))
+    m = DeepseekModel(cfg, ecfg, ps, layers, embed, ones(h), head, dev, kv_dtype=torch.float8_e4m3fn)
+    m.weight_sets = len(expert_sets)
+    return m
+
+
+def _gate_up(I: int, h: int, dev, sd) -> MXFP8Tensor:
+    """[gate; up] stacked rows with I a multiple of 128 per half."""
+    assert I % 128 == 0, I
+    return rand_mx((), 2 * I, h, dev, sd)

@@ -243,12 +243,13 @@ def router(h, gate: torch.Tensor, bias: torch.Tensor, cfg):
                            cfg.routed_scaling_factor, cfg.norm_topk_prob)
 
 
-def moe_experts(h, w: torch.Tensor, ids: torch.Tensor, ex: ExpertWeights, out_dtype=torch.float32):
+def moe_experts(h, w: torch.Tensor, ids: torch.Tensor, ex: ExpertWeights, out_dtype=torch.float32,
+                n_experts_total=None):
     """Local-expert part of the MoE: sum_k w[t,k] * expert_{ids[t,k]}(h[t]) over
     the experts this rank owns (others contribute on their ranks)."""
     if isinstance(ex.w13, MXFP8Tensor) and (h.q if isinstance(h, QAct) else h).is_cuda:
         if _IMPL == "native":
-            return _native().moe_experts(h, w, ids, ex, out_dtype)
+            return _native().moe_experts(h, w, ids, ex, out_dtype, n_experts_total)
         from . import baseline
         return baseline.moe_experts(h if isinstance(h, QAct) else quant(h), w, ids, ex, out_dtype)
     xf = to_float(h)

@@ -97,13 +97,14 @@ def _gemm_raw(a, w: MXFP8Tensor, out: torch.Tensor, epi: int, splits: int = 1, p
 
 
 def choose_splits(T: int, N: int, K: int) -> int:
-    """Split-K factor so small-token GEMMs still cover the 148 SMs."""
-    tiles = (N // 128) * max(1, (T + 127) // 128)
-    if tiles >= 148 or T > 256:
+    """Cluster split-K factor (1, 2, 4 or 8) so small-token GEMMs cover the
+    148 SMs; every split keeps at least two k-tiles."""
+    if T > 128:
         return 1
+    tiles = N // 128
     ktiles = K // 128
     s = 1
-    while tiles * s * 2 <= 2 * 148 and s * 2 <= ktiles // 4:
+    while s < 8 and tiles * s * 2 <= 148 + 74 and ktiles // (s * 2) >= 2:
         s *= 2
     return s
 
@@ -112,13 +113,13 @@ def gemm(a, w: MXFP8Tensor, out_dtype=torch.bfloat16) -> torch.Tensor:
     T, K = a.q.shape
     N = w.data.shape[0]
     assert w.data.shape[1] == K, (w.data.shape, a.q.shape)
-    splits = choose_splits(T, N, K)
-    if splits > 1 or out_dtype == torch.float32:
+    if out_dtype == torch.float32:
         out = torch.zeros(T, N, dtype=torch.float32, device=a.q.device)
-        _gemm_raw(a, w, out, 1, splits)
-        return out if out_dtype == torch.float32 else out.to(out_dtype)
+        _gemm_raw(a, w, out, 1, choose_splits(T, N, K))
+        return out
     out = torch.empty(T, N, dtype=torch.bfloat16, device=a.q.device)
-    _gemm_raw(a, w, out, 0)
+    splits = choose_splits(T, N, K)
+    _gemm_raw(a, w, out, 4 if splits > 1 else 0, splits, pdl=True)
     return out
 
 
@@ -147,13 +148,36 @@ def kv_store(kv_a, ln_w, eps, table, pos, cache, slots, kv_scale, kv_lora):
     _C.kv_store(kv_a, ln_w, eps, pos, table, slots, cache.view(torch.uint8), kv_scale, kv_lora)
 
 
-def mla_attention(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size, topk=None):
+def mla_splits(T: int, H: int, max_len: int) -> int:
+    """KV splits so that decode grids cover the SMs (at least ~2 tiles each)."""
+    groups = H // 64 if H % 64 == 0 else (H // 32 if H % 32 == 0 else H // 16)
+    ctas = T * max(1, groups)
+    s = max(1, min(16, -(-296 // ctas), max(1, max_len // 256)))
+    return s
+
+
+def mla_attention(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size, topk=None, impl=None):
     T, H, L = q_abs.shape
-    out = torch.empty(T, H, L, dtype=torch.bfloat16, device=q_abs.device)
+    dev = q_abs.device
+    out = torch.empty(T, H, L, dtype=torch.bfloat16, device=dev)
     qa = q_abs.to(torch.bfloat16).contiguous()
     qp = q_pe.to(torch.bfloat16).contiguous()
-    _C.mla_simt(qa, qp, cache.view(torch.uint8), kv_scale, fb.block_table, fb.q_seq, fb.positions, topk,
-                page_size, softmax_scale, out)
+    use_tc = (impl or "tc") == "tc" and topk is None and page_size == 64 and L == 512 and H % 16 == 0 \
+        and q_pe.shape[-1] == 64
+    if not use_tc:
+        _C.mla_simt(qa, qp, cache.view(torch.uint8), kv_scale, fb.block_table, fb.q_seq, fb.positions, topk,
+                    page_size, softmax_scale, out)
+        return out
+    q8 = torch.empty(T, H, 576, dtype=torch.uint8, device=dev)
+    qs = torch.empty(T, H, dtype=torch.float32, device=dev)
+    _C.mla_q_quant(qa, qp, q8, qs)
+    nsplit = mla_splits(T, H, int(fb.max_seq_len) if fb.max_seq_len else 4096) if fb.is_decode else 1
+    po = pl = None
+    if nsplit > 1:
+        po = torch.empty(nsplit, T, H, L, dtype=torch.float32, device=dev)
+        pl = torch.empty(nsplit, T, H, dtype=torch.float32, device=dev)
+    _C.mla_tc(q8, qs, cache.view(torch.uint8), kv_scale, fb.block_table, fb.q_seq, fb.positions, page_size,
+              softmax_scale, nsplit, out, po, pl)
     return out
 
 
@@ -170,10 +194,18 @@ def router(x: torch.Tensor, gate: torch.Tensor, bias: torch.Tensor, cfg):
     return w, ids
 
 
-def moe_experts(h, w: torch.Tensor, ids: torch.Tensor, ex, out_dtype=torch.bfloat16) -> torch.Tensor:
-    """Local-expert MoE: align -> gather -> FC1 (SwiGLU+quant) -> FC2
-    (routing-weighted) -> combine.  Host-synchronisation free: buffers are
-    sized for the worst case (every pair local)."""
+def moe_tile_n(rows_per_expert: float, cap: int) -> int:
+    """Token tile of the grouped GEMMs from the expected rows per expert."""
+    for bn in (16, 32, 64, 128):
+        if rows_per_expert * 1.5 <= bn or bn == cap:
+            return bn
+    return cap
+
+
+def moe_experts(h, w: torch.Tensor, ids: torch.Tensor, ex, out_dtype=torch.bfloat16, n_experts_total=None):
+    """Local-expert MoE: routing layout -> row gather -> persistent FC1
+    (SwiGLU + MXFP8 requant) -> persistent FC2 (routing-weighted) -> combine.
+    No host synchronisation: buffers are sized for the worst case."""
     from . import QAct
     a = h if isinstance(h, QAct) else quant(h)
     T, Hd = a.q.shape
@@ -181,24 +213,31 @@ def moe_experts(h, w: torch.Tensor, ids: torch.Tensor, ex, out_dtype=torch.bfloa
     E = ex.count
     dev = a.q.device
     I = ex.inter
+    e_tot = n_experts_total or E
+    exp_rows = T * K / e_tot
+    bn1 = moe_tile_n(exp_rows, 64)
+    bn2 = moe_tile_n(exp_rows, 128)
     max_rows = round_up(T * K, 128) + E * 128   # 128-aligned segments
     seg_start = torch.empty(E, dtype=torch.int32, device=dev)
     seg_count = torch.empty(E, dtype=torch.int32, device=dev)
-    row_token = torch.full((max_rows,), -1, dtype=torch.int32, device=dev)
-    row_weight = torch.zeros(max_rows, dtype=torch.float32, device=dev)
+    tt1 = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    tt2 = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    row_token = torch.empty(max_rows, dtype=torch.int32, device=dev)
+    row_weight = torch.empty(max_rows, dtype=torch.float32, device=dev)
     pair_row = torch.empty(T, K, dtype=torch.int32, device=dev)
     total = torch.empty(1, dtype=torch.int32, device=dev)
-    _C.moe_align(ids, w.float().contiguous(), ex.first, E, seg_start, seg_count, row_token, row_weight, pair_row, total)
+    ids = ids if ids.dtype == torch.int32 else ids.int()
+    _C.moe_align(ids.contiguous(), w.float().contiguous(), ex.first, E, seg_start, seg_count, row_token, row_weight,
+                 pair_row, total, bn1, tt1, bn2, tt2)
     xs = alloc_qact(max_rows, Hd, dev)
-    _C.moe_gather(a.q, a.sf, row_token, max_rows, xs.q, xs.sf)
+    _C.moe_gather(a.q, a.sf, pair_row, xs.q, xs.sf)
     hq = alloc_qact(max_rows, I, dev)
-    max_per = min(T, max_rows)   # an expert receives each token at most once
     w13, w2 = ex.w13, ex.w2
-    _C.gemm(w13.data, w13.sf, w13.sf.stride(0) if w13.sf.dim() > 1 else 0, xs.q, xs.sf, 2 * I, max_rows, Hd, 2, 1,
-            None, 0, hq.q, hq.sf, I, I, E, seg_start, seg_count, max_per, None, None, False)
+    _C.gemm_grouped(w13.data, w13.sf, xs.q, xs.sf, 2 * I, Hd, E, I, bn1, seg_start, seg_count, tt1, 2,
+                    None, 0, hq.q, hq.sf, I, None, 0, True)
     y = torch.empty(max_rows, Hd, dtype=torch.bfloat16, device=dev)
-    _C.gemm(w2.data, w2.sf, w2.sf.stride(0) if w2.sf.dim() > 1 else 0, hq.q, hq.sf, Hd, max_rows, I, 3, 1,
-            y, Hd, None, None, 0, 0, E, seg_start, seg_count, max_per, row_weight, None, False)
+    _C.gemm_grouped(w2.data, w2.sf, hq.q, hq.sf, Hd, I, E, 0, bn2, seg_start, seg_count, tt2, 3,
+                    y, Hd, None, None, 0, row_weight, 0, True)
     out = torch.empty(T, Hd, dtype=out_dtype, device=dev)
     _C.moe_combine(y, pair_row, None, out)
     return out

@@ -1,0 +1,505 @@
+// Absorbed MLA decode attention on tcgen05 over the paged e4m3 latent cache.
+//
+// Work item = (query token t, group of HB heads, KV split s).  Per 128-token
+// KV tile (two 64-token pages fetched by TMA: four 128-byte latent boxes with
+// 128B swizzle + one 64-byte rope box with 64B swizzle):
+//
+//   MMA1  S^T[128 tok, HB] = K[128 tok, 576] . Q[HB, 576]^T      (kind::f8f6f4)
+//   softmax warpgroup: S^T -> registers -> smem transpose; per-head running
+//         max in the log2 domain, raised only when a tile exceeds it by more
+//         than 8 (so P = 2^(x - m) <= 256 fits e4m3 and O rarely needs a
+//         rescale); P written as e4m3 into the MMA2 B operand (MN-major)
+//   MMA2  O^T[512, HB] += V^T[512, 128 tok] . P^T[128 tok, HB]    (4 x M=128)
+//
+// KV tokens are the MMA's M (128) dimension and heads the N dimension, so a
+// tensor-parallel rank with 16 heads still issues M=128 MMAs.  O^T lives in
+// TMEM for the whole split; the epilogue normalises by the running sum and
+// writes bf16 (or a partial + log-sum-exp for the split merge).
+//
+// Warp roles (192 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA
+// issuer, warps 2-5 softmax / correction / epilogue.  All waits bounded.
+//
+// Reference parity: the reference's own sparse-MLA decode kernel `bsx`
+// (ro_unit.cu:480; c36s SPA design ro_unit.cu:136-172) uses the same
+// transposed S^T / O^T arrangement with e4m3 P; this kernel is written from
+// the PTX ISA, not from that code.
+#include "../common/ptx.cuh"
+#include "attn.h"
+
+namespace b200 {
+namespace mla {
+
+constexpr int kThreads = 192;
+constexpr int kTile = 128;          // KV tokens per tile
+constexpr int kPage = 64;           // tokens per KV page (one TMA box height)
+constexpr int kL = 512;             // latent
+constexpr int kR = 64;              // rope
+constexpr int kD = kL + kR;         // bytes per cached token
+constexpr int kStages = 2;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleThresh = 8.0f;
+
+template <int HB>
+struct Smem {
+  static constexpr int kQLat = 4 * HB * 128;            // 4 latent boxes [HB x 128B]
+  static constexpr int kQRope = HB * 64;                // rope box [HB x 64B]
+  static constexpr int kKVLat = 4 * kTile * 128;        // 64 KB
+  static constexpr int kKVRope = kTile * 64;            // 8 KB
+  static constexpr int kKVStage = kKVLat + kKVRope;     // 72 KB
+  static constexpr int kP = kTile * HB;                 // e4m3 P^T
+  static constexpr int kS = kTile * (HB + 1) * 4;       // fp32 transpose (padded)
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffKV = ((kQLat + kQRope + 1023) / 1024) * 1024;
+  static constexpr int kOffP = kOffKV + kStages * kKVStage;
+  static constexpr int kOffS = kOffP + ((kP + 127) / 128) * 128;
+  static constexpr int kOffRed = kOffS + kS;            // 2 x 128 floats
+  static constexpr int kOffHead = kOffRed + 2 * 128 * 4;  // per-head state
+  static constexpr int kOffBar = kOffHead + 8 * HB * 4;
+  static constexpr int kBytes = kOffBar + 256 + 1024;
+  static constexpr int kTmemS = 0;                      // 2 x HB columns
+  static constexpr int kTmemO = 2 * HB;                 // 4 x HB columns
+  static constexpr int kTmemNeed = 6 * HB;
+  static constexpr int kTmemCols = kTmemNeed <= 32 ? 32 : kTmemNeed <= 64 ? 64 : kTmemNeed <= 128 ? 128
+                                   : kTmemNeed <= 256 ? 256 : 512;
+};
+
+struct Params {
+  const int* block_table;
+  int bt_stride;
+  const int* q_seq;
+  const int* q_pos;
+  const float* q_scale;      // [T, H]
+  int H;
+  int nsplit;
+  int split_tokens;          // KV tokens per split (multiple of 128)
+  float qk_factor;           // sm_scale * kv_scale * log2(e)
+  float kv_scale;
+  __nv_bfloat16* out;        // [T, H, 512] when nsplit == 1
+  float* part_o;             // [nsplit, T, H, 512] when nsplit > 1
+  float* part_lse;           // [nsplit, T, H]
+  uint32_t* err;
+};
+
+__device__ __forceinline__ void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+
+template <int HB>
+__global__ void __launch_bounds__(kThreads, 1)
+mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constant__ CUtensorMap tm_q_rope,
+              const __grid_constant__ CUtensorMap tm_kv_lat, const __grid_constant__ CUtensorMap tm_kv_rope,
+              Params p) {
+  using S = Smem<HB>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = sm + S::kOffQ;
+  uint8_t* sKV = sm + S::kOffKV;
+  uint8_t* sP = sm + S::kOffP;
+  float* sS = reinterpret_cast<float*>(sm + S::kOffS);
+  float* sRed = reinterpret_cast<float*>(sm + S::kOffRed);
+  float* sHead = reinterpret_cast<float*>(sm + S::kOffHead);   // [0:HB) factor, [HB:2HB) m, [2HB:3HB) l, [3HB:4HB) alpha
+  int* sFlag = reinterpret_cast<int*>(sHead + 4 * HB);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kOffBar);
+  uint64_t* kv_full = bars;              // [2]
+  uint64_t* kv_empty = bars + 2;         // [2]
+  uint64_t* q_full = bars + 4;
+  uint64_t* s_full = bars + 5;           // [2]
+  uint64_t* s_free = bars + 7;           // [2]
+  uint64_t* p_full = bars + 9;
+  uint64_t* o_done = bars + 10;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 12);
+
+  const int warp = warp_id(), lane = lane_id();
+  const int t = blockIdx.x;
+  const int h0 = blockIdx.y * HB;
+  const int split = blockIdx.z;
+
+  pdl_wait();
+  const int b = p.q_seq[t];
+  const int n = p.q_pos[t] + 1;
+  // KV tokens per split adapt to this query's own length (graph-safe).
+  const int chunk = (((n + p.nsplit - 1) / p.nsplit) + kTile - 1) / kTile * kTile;
+  const int k_lo = split * chunk;
+  const int k_hi = min(n, k_lo + chunk);
+  const int nt = k_hi > k_lo ? (k_hi - k_lo + kTile - 1) / kTile : 0;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 1);
+    }
+    mbar_init(q_full, 1);
+    mbar_init(p_full, 1);
+    mbar_init(o_done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, S::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0 && nt > 0) {
+      const int qrow = t * p.H + h0;
+      mbar_arrive_expect_tx(q_full, S::kQLat + S::kQRope);
+      for (int c = 0; c < 4; ++c) tma_load_2d(sQ + c * HB * 128, &tm_q_lat, q_full, c * 128, qrow);
+      tma_load_2d(sQ + S::kQLat, &tm_q_rope, q_full, kL, qrow);
+      for (int i = 0; i < nt; ++i) {
+        const int s = i % kStages;
+        if (i >= kStages && !mbar_wait(&kv_empty[s], ((i / kStages) - 1) & 1, p.err)) break;
+        mbar_arrive_expect_tx(&kv_full[s], S::kKVStage);
+        uint8_t* dst = sKV + s * S::kKVStage;
+        const int tok0 = k_lo + i * kTile;
+        for (int pg = 0; pg < 2; ++pg) {
+          const int lp = (tok0 + pg * kPage) / kPage;        // logical page (may be past the end: page 0)
+          const int page = (tok0 + pg * kPage < n) ? p.block_table[(int64_t)b * p.bt_stride + lp] : 0;
+          const int row = page * kPage;
+          for (int c = 0; c < 4; ++c)
+            tma_load_2d(dst + c * kTile * 128 + pg * kPage * 128, &tm_kv_lat, &kv_full[s], c * 128, row);
+          tma_load_2d(dst + S::kKVLat + pg * kPage * 64, &tm_kv_rope, &kv_full[s], kL, row);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer ----------------------------
+    const uint32_t idesc1 = idesc_f8(128, HB, false, false);
+    const uint32_t idesc2 = idesc_f8(128, HB, true, true);
+    bool ok = nt > 0 && mbar_wait(q_full, 0, p.err);
+    auto mma2 = [&](int i) -> bool {
+      if (!mbar_wait(p_full, i & 1, p.err)) return false;
+      tc_fence_after();
+      if (lane == 0) {
+        const int s = i % kStages;
+        const uint32_t kv = smem_u32(sKV + s * S::kKVStage);
+        const uint32_t pb = smem_u32(sP);
+        for (int c = 0; c < 4; ++c) {
+          for (int kk = 0; kk < kTile / 32; ++kk) {
+            // A = V^T: MN-major SW128, 8-token groups 1024 B apart
+            const uint64_t ad = smem_desc(kv + c * kTile * 128 + kk * 32 * 128, 0, 1024, 2);
+            // B = P^T: MN-major no swizzle; core matrix = 8 tokens x 16 heads
+            const uint64_t bd = smem_desc(pb + kk * 4 * (HB / 16) * 128, (HB / 16) * 128, 128, 0);
+            mma_f8(tmem + S::kTmemO + c * HB, ad, bd, idesc2, (i > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+        mma_commit(o_done);
+        mma_commit(&kv_empty[s]);
+      }
+      __syncwarp();
+      return true;
+    };
+    for (int i = 0; ok && i < nt; ++i) {
+      const int s = i % kStages;
+      if (!mbar_wait(&kv_full[s], (i / kStages) & 1, p.err)) { ok = false; break; }
+      if (i >= 2 && !mbar_wait(&s_free[i & 1], ((i >> 1) - 1) & 1, p.err)) { ok = false; break; }
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t kv = smem_u32(sKV + s * S::kKVStage);
+        const uint32_t q = smem_u32(sQ);
+        const uint32_t d = tmem + S::kTmemS + (i & 1) * HB;
+        int step = 0;
+        for (int c = 0; c < 4; ++c)
+          for (int kk = 0; kk < 4; ++kk, ++step)
+            mma_f8(d, desc_kmajor_sw128(kv + c * kTile * 128 + kk * 32), desc_kmajor_sw128(q + c * HB * 128 + kk * 32),
+                   idesc1, step > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 2; ++kk)
+          mma_f8(d, smem_desc(kv + S::kKVLat + kk * 32, 16, 512, 4), smem_desc(q + S::kQLat + kk * 32, 16, 512, 4),
+                 idesc1, 1u);
+        mma_commit(&s_full[i & 1]);
+      }
+      __syncwarp();
+      if (i >= 1 && !mma2(i - 1)) { ok = false; break; }
+    }
+    if (ok && nt > 0) mma2(nt - 1);
+  } else {
+    // ---------------------- softmax / correction / epilogue ----------------------
+    const int tid = threadIdx.x - 64;            // 0..127
+    const int sub = warp & 3;                    // TMEM subpartition
+    const int row = sub * 32 + lane;             // token row of S^T / latent row of O^T
+    constexpr int QN = 128 / HB;                 // threads per head in the reduction
+    const int hh = tid % HB, part = tid / HB;
+    if (tid < HB) {
+      sHead[tid] = p.q_scale[(int64_t)t * p.H + h0 + tid] * p.qk_factor;
+      sHead[HB + tid] = -INFINITY;
+      sHead[2 * HB + tid] = 0.f;
+    }
+    if (tid == 0) sFlag[0] = 0;
+    named_bar(1, 128);
+    bool ok = true;
+    for (int i = 0; i < nt; ++i) {
+      if (!mbar_wait(&s_full[i & 1], (i >> 1) & 1, p.err)) { ok = false; break; }
+      tc_fence_after();
+      const int tok0 = k_lo + i * kTile;
+      // 1. S^T row -> scaled log2 scores in the padded transpose buffer
+      {
+        const uint32_t base = tmem + S::kTmemS + (i & 1) * HB + (uint32_t(sub * 32) << 16);
+#pragma unroll
+        for (int c0 = 0; c0 < HB; c0 += 16) {
+          uint32_t r[16];
+          tmem_ld_x16(base + c0, r);
+          tmem_ld_wait();
+          const bool valid = tok0 + row < k_hi;
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            sS[row * (HB + 1) + c0 + j] = valid ? __uint_as_float(r[j]) * sHead[c0 + j] : -INFINITY;
+        }
+      }
+      tc_fence_before();
+      named_bar(1, 128);
+      if (tid == 0) mbar_arrive(&s_free[i & 1]);
+      // 2. per-head tile max
+      float mx = -INFINITY;
+      for (int j = part; j < kTile; j += QN) mx = fmaxf(mx, sS[j * (HB + 1) + hh]);
+      sRed[part * HB + hh] = mx;
+      named_bar(1, 128);
+      if (tid < HB) {
+        float m = -INFINITY;
+        for (int q = 0; q < QN; ++q) m = fmaxf(m, sRed[q * HB + tid]);
+        const float mold = sHead[HB + tid];
+        float alpha = 1.f;
+        if (m > mold + kRescaleThresh || mold == -INFINITY) {
+          const float mnew = m;
+          alpha = (mold == -INFINITY) ? 0.f : exp2f(mold - mnew);
+          sHead[HB + tid] = mnew;
+          if (mold != -INFINITY) sFlag[0] = 1;
+        }
+        sHead[3 * HB + tid] = alpha;
+      }
+      named_bar(1, 128);
+      // 3. P = 2^(x - m) -> e4m3 (<= 256); partial sums of the quantized P
+      const float m = sHead[HB + hh];
+      float lsum = 0.f;
+      // the previous MMA2 must have finished reading sP (and writing O^T)
+      if (i >= 1 && !mbar_wait(o_done, (i - 1) & 1, p.err)) { ok = false; }
+      for (int j = part; j < kTile; j += QN) {
+        const float x = sS[j * (HB + 1) + hh];
+        const float pv = (x == -INFINITY) ? 0.f : exp2f(x - m);
+        const uint16_t q2 = f2_to_e4m3x2(pv, 0.f);
+        const uint8_t qb = uint8_t(q2 & 0xFF);
+        __nv_fp8_e4m3 f8;
+        f8.__x = qb;
+        lsum += float(f8);
+        // MN-major no-swizzle core-matrix layout: [k group j/8][n chunk h/16][8 x 16]
+        sP[(j >> 3) * (HB / 16) * 128 + (hh >> 4) * 128 + (j & 7) * 16 + (hh & 15)] = qb;
+      }
+      sRed[128 + part * HB + hh] = lsum;
+      named_bar(1, 128);
+      if (tid < HB) {
+        float l = 0.f;
+        for (int q = 0; q < QN; ++q) l += sRed[128 + q * HB + tid];
+        sHead[2 * HB + tid] = sHead[2 * HB + tid] * sHead[3 * HB + tid] + l;
+      }
+      // 4. rescale O^T columns whose max moved (rare)
+      if (sFlag[0] && i >= 1) {
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t ob = tmem + S::kTmemO + c * HB + (uint32_t(sub * 32) << 16);
+#pragma unroll
+          for (int c0 = 0; c0 < HB; c0 += 8) {
+            uint32_t r[8];
+            tmem_ld_x8(ob + c0, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * sHead[3 * HB + c0 + j]);
+            tmem_st_x8(ob + c0, r);
+          }
+        }
+        tmem_st_wait();
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      named_bar(1, 128);
+      if (tid == 0) {
+        sFlag[0] = 0;
+        mbar_arrive(p_full);
+      }
+      if (!ok) break;
+    }
+    // 5. epilogue: O^T (lane = latent row within block c, column = head)
+    if (nt > 0 && ok && mbar_wait(o_done, (nt - 1) & 1, p.err)) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        const uint32_t ob = tmem + S::kTmemO + c * HB + (uint32_t(sub * 32) << 16);
+        const int d = c * 128 + row;
+#pragma unroll
+        for (int c0 = 0; c0 < HB; c0 += 8) {
+          uint32_t r[8];
+          tmem_ld_x8(ob + c0, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int h = c0 + j;
+            const float l = sHead[2 * HB + h];
+            const float o = l > 0.f ? __uint_as_float(r[j]) * p.kv_scale / l : 0.f;
+            const int64_t oi = ((int64_t)t * p.H + h0 + h) * kL + d;
+            if (p.nsplit == 1) {
+              p.out[oi] = __float2bfloat16(o);
+            } else {
+              p.part_o[(int64_t)split * ((int64_t)gridDim.x * p.H * kL) + oi] = o;
+            }
+          }
+        }
+      }
+      if (p.nsplit > 1 && tid < HB) {
+        const float l = sHead[2 * HB + tid];
+        p.part_lse[(int64_t)split * gridDim.x * p.H + (int64_t)t * p.H + h0 + tid] =
+            l > 0.f ? sHead[HB + tid] + log2f(l) : -INFINITY;
+      }
+    } else if (p.nsplit > 1 && tid < HB) {
+      // empty split
+      p.part_lse[(int64_t)split * gridDim.x * p.H + (int64_t)t * p.H + h0 + tid] = -INFINITY;
+    }
+    if (nt == 0 && p.nsplit == 1) {
+      for (int e = tid; e < HB * kL; e += 128)
+        p.out[((int64_t)t * p.H + h0) * kL + e] = __float2bfloat16(0.f);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, S::kTmemCols);
+  }
+}
+
+// Merge split partials: out = sum_s 2^(lse_s - M) o_s / sum_s 2^(lse_s - M).
+__global__ void mla_merge_kernel(const float* part_o, const float* part_lse, int nsplit, int TH, __nv_bfloat16* out) {
+  const int th = blockIdx.x;
+  pdl_wait();
+  float M = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, part_lse[(int64_t)s * TH + th]);
+  float w[16];
+  float den = 0.f;
+  for (int s = 0; s < nsplit && s < 16; ++s) {
+    const float l = part_lse[(int64_t)s * TH + th];
+    w[s] = (l == -INFINITY) ? 0.f : exp2f(l - M);
+    den += w[s];
+  }
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  for (int d = threadIdx.x; d < kL; d += blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < nsplit && s < 16; ++s)
+      if (w[s] != 0.f) acc += w[s] * part_o[((int64_t)s * TH + th) * kL + d];
+    out[(int64_t)th * kL + d] = __float2bfloat16(acc * inv);
+  }
+  pdl_launch_dependents();
+}
+
+// q_abs [T,H,512] bf16 + q_pe [T,H,64] bf16 -> e4m3 [T,H,576] with a per-(t,h) fp32 scale.
+__global__ void q_quant_kernel(const __nv_bfloat16* q_abs, const __nv_bfloat16* q_pe, int TH, uint8_t* q8, float* qs) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  pdl_wait();
+  if (w >= TH) return;
+  const __nv_bfloat16* a = q_abs + (int64_t)w * kL;
+  const __nv_bfloat16* r = q_pe + (int64_t)w * kR;
+  float v[18];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __bfloat162float(a[lane + 32 * i]);
+  v[16] = __bfloat162float(r[lane]);
+  v[17] = __bfloat162float(r[lane + 32]);
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 18; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float sc = amax > 0.f ? amax / 448.f : 1.f;
+  const float inv = 1.f / sc;
+  uint8_t* dst = q8 + (int64_t)w * kD;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) dst[lane + 32 * i] = uint8_t(f2_to_e4m3x2(v[i] * inv, 0.f) & 0xFF);
+  dst[kL + lane] = uint8_t(f2_to_e4m3x2(v[16] * inv, 0.f) & 0xFF);
+  dst[kL + lane + 32] = uint8_t(f2_to_e4m3x2(v[17] * inv, 0.f) & 0xFF);
+  if (lane == 0) qs[w] = sc;
+  pdl_launch_dependents();
+}
+
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+static int map2d(CUtensorMap* m, const void* base, int64_t rows, int box_rows, int box_cols, CUtensorMapSwizzle sw) {
+  cuuint64_t dims[2] = {(cuuint64_t)kD, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)kD};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : int(r);
+}
+
+template <int HB>
+static int launch(const MlaTcArgs& a, cudaStream_t st) {
+  using S = Smem<HB>;
+  CUtensorMap mql, mqr, mkl, mkr;
+  const int64_t qrows = (int64_t)a.T * a.H;
+  if (map2d(&mql, a.q8, qrows, HB, 128, CU_TENSOR_MAP_SWIZZLE_128B)) return -2;
+  if (map2d(&mqr, a.q8, qrows, HB, 64, CU_TENSOR_MAP_SWIZZLE_64B)) return -3;
+  if (map2d(&mkl, a.cache, a.cache_rows, kPage, 128, CU_TENSOR_MAP_SWIZZLE_128B)) return -4;
+  if (map2d(&mkr, a.cache, a.cache_rows, kPage, 64, CU_TENSOR_MAP_SWIZZLE_64B)) return -5;
+  Params p{};
+  p.block_table = a.block_table;
+  p.bt_stride = a.bt_stride;
+  p.q_seq = a.q_seq;
+  p.q_pos = a.q_pos;
+  p.q_scale = a.q_scale;
+  p.H = a.H;
+  p.nsplit = a.nsplit;
+  p.split_tokens = a.split_tokens;
+  p.qk_factor = a.sm_scale * a.kv_scale * kLog2e;
+  p.kv_scale = a.kv_scale;
+  p.out = reinterpret_cast<__nv_bfloat16*>(a.out);
+  p.part_o = a.part_o;
+  p.part_lse = a.part_lse;
+  p.err = a.err;
+  auto kern = mla_tc_kernel<HB>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes);
+  dim3 grid(a.T, a.H / HB, a.nsplit);
+  kern<<<grid, kThreads, S::kBytes, st>>>(mql, mqr, mkl, mkr, p);
+  if (cudaGetLastError() != cudaSuccess) return 1;
+  if (a.nsplit > 1) {
+    mla_merge_kernel<<<a.T * a.H, 128, 0, st>>>(a.part_o, a.part_lse, a.nsplit, a.T * a.H,
+                                                 reinterpret_cast<__nv_bfloat16*>(a.out));
+    if (cudaGetLastError() != cudaSuccess) return 2;
+  }
+  return 0;
+}
+
+}  // namespace mla
+}  // namespace b200
+
+int b200_mla_q_quant(const void* q_abs, const void* q_pe, int TH, uint8_t* q8, float* qs, cudaStream_t st) {
+  if (TH <= 0) return 0;
+  b200::mla::q_quant_kernel<<<(TH * 32 + 127) / 128, 128, 0, st>>>(
+      reinterpret_cast<const __nv_bfloat16*>(q_abs), reinterpret_cast<const __nv_bfloat16*>(q_pe), TH, q8, qs);
+  return cudaGetLastError() == cudaSuccess ? 0 : 1;
+}
+
+int b200_mla_tc(const MlaTcArgs* a, cudaStream_t st) {
+  using namespace b200::mla;
+  if (a->T <= 0) return 0;
+  if (a->page_size != kPage || a->nsplit < 1 || a->nsplit > 16) return -1;
+  if (a->H % 64 == 0) return launch<64>(*a, st);
+  if (a->H % 32 == 0) return launch<32>(*a, st);
+  if (a->H % 16 == 0) return launch<16>(*a, st);
+  return -6;
+}

@@ -5,6 +5,9 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cstring>
+#include <vector>
+
 #include "attn/attn.h"
 #include "comm/comm.h"
 #include "elementwise/elementwise.h"
@@ -132,22 +135,68 @@ void router(const at::Tensor& logits, const at::Tensor& bias, int64_t G, int64_t
 
 void moe_align(const at::Tensor& ids, const at::Tensor& w, int64_t first, int64_t E, at::Tensor seg_start,
                at::Tensor seg_count, at::Tensor row_token, at::Tensor row_weight, at::Tensor pair_row,
-               at::Tensor total_rows) {
+               at::Tensor total_rows, int64_t bn1, c10::optional<at::Tensor> ttile1, int64_t bn2,
+               c10::optional<at::Tensor> ttile2) {
   check_cuda(ids, "ids");
   const c10::cuda::CUDAGuard g(ids.device());
+  TORCH_CHECK(ids.scalar_type() == at::kInt && ids.is_contiguous(), "ids int32");
   check(b200_moe_align(ptr<int>(ids), ptr<float>(w), ids.size(0), ids.size(1), first, E, ptr<int>(seg_start),
                        ptr<int>(seg_count), ptr<int>(row_token), ptr<float>(row_weight), ptr<int>(pair_row),
-                       ptr<int>(total_rows), cur_stream()),
+                       ptr<int>(total_rows), bn1, optr<int>(ttile1), bn2, optr<int>(ttile2), cur_stream()),
         "moe_align");
 }
 
-void moe_gather(const at::Tensor& xq, const at::Tensor& xsf, const at::Tensor& row_token, int64_t rows_total,
-                at::Tensor dq, at::Tensor dsf) {
+void moe_gather(const at::Tensor& xq, const at::Tensor& xsf, const at::Tensor& pair_row, at::Tensor dq, at::Tensor dsf) {
   check_cuda(xq, "xq");
   const c10::cuda::CUDAGuard g(xq.device());
-  check(b200_moe_gather(ptr<uint8_t>(xq), ptr<uint8_t>(xsf), ptr<int>(row_token), rows_total, xq.size(1),
-                        ptr<uint8_t>(dq), ptr<uint8_t>(dsf), cur_stream()),
+  check(b200_moe_gather(ptr<uint8_t>(xq), ptr<uint8_t>(xsf), ptr<int>(pair_row), pair_row.numel(), pair_row.size(1),
+                        xq.size(1), ptr<uint8_t>(dq), ptr<uint8_t>(dsf), cur_stream()),
         "moe_gather");
+}
+
+int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+void gemm_grouped(const at::Tensor& w, const at::Tensor& w_sf, const at::Tensor& x, const at::Tensor& x_sf,
+                  int64_t nw, int64_t k, int64_t E, int64_t inter, int64_t bn, const at::Tensor& seg_start,
+                  const at::Tensor& seg_count, const at::Tensor& ttile_off, int64_t epi, c10::optional<at::Tensor> out,
+                  int64_t ldo, c10::optional<at::Tensor> q_out, c10::optional<at::Tensor> sf_out, int64_t ldq,
+                  c10::optional<at::Tensor> row_weight, int64_t num_ctas, bool pdl) {
+  check_cuda(w, "w");
+  const c10::cuda::CUDAGuard g(w.device());
+  TORCH_CHECK(k % 128 == 0 && nw % 128 == 0, "k and nw must be multiples of 128");
+  GroupedArgs a{};
+  a.w = ptr<uint8_t>(w);
+  a.w_sf = ptr<uint8_t>(w_sf);
+  a.w_sf_estride = w_sf.dim() > 1 ? w_sf.stride(0) : 0;
+  a.x = ptr<uint8_t>(x);
+  a.x_sf = ptr<uint8_t>(x_sf);
+  a.x_rows = x.size(0);
+  a.nw = nw;
+  a.k = k;
+  a.E = E;
+  a.inter = inter;
+  a.bn = bn;
+  a.seg_start = ptr<int>(seg_start);
+  a.seg_count = ptr<int>(seg_count);
+  a.ttile_off = ptr<int>(ttile_off);
+  a.epi = epi;
+  a.out = optr<void>(out);
+  a.ldo = ldo;
+  a.q_out = optr<uint8_t>(q_out);
+  a.sf_out = optr<uint8_t>(sf_out);
+  a.ldq = ldq;
+  a.row_weight = optr<float>(row_weight);
+  a.num_ctas = num_ctas > 0 ? num_ctas : num_sms();
+  a.pdl = pdl ? 1 : 0;
+  check(b200_gemm_grouped(&a, cur_stream()), "gemm_grouped");
 }
 
 void moe_combine(const at::Tensor& y, const at::Tensor& pair_row, c10::optional<at::Tensor> add, at::Tensor out) {
@@ -159,6 +208,36 @@ void moe_combine(const at::Tensor& y, const at::Tensor& pair_row, c10::optional<
                          add.has_value() && add->scalar_type() == at::kFloat, out.data_ptr(),
                          out.scalar_type() == at::kFloat, cur_stream()),
         "moe_combine");
+}
+
+void fill_bytes(at::Tensor t, int64_t seed, int64_t and_mask, int64_t or_mask) {
+  check_cuda(t, "t");
+  const c10::cuda::CUDAGuard g(t.device());
+  TORCH_CHECK(t.is_contiguous(), "contiguous");
+  check(b200_fill_bytes(t.data_ptr(), t.numel() * t.element_size(), (uint64_t)seed, (uint8_t)and_mask, (uint8_t)or_mask,
+                        cur_stream()),
+        "fill_bytes");
+}
+
+// Kernel nodes of a captured CUDA graph: (all kernels, kernels of this
+// extension).  Used by the benchmark to report its launches per step.
+std::vector<int64_t> graph_kernel_count(int64_t raw_graph) {
+  cudaGraph_t g = reinterpret_cast<cudaGraph_t>(raw_graph);
+  size_t n = 0;
+  TORCH_CHECK(cudaGraphGetNodes(g, nullptr, &n) == cudaSuccess, "cudaGraphGetNodes");
+  std::vector<cudaGraphNode_t> nodes(n);
+  TORCH_CHECK(cudaGraphGetNodes(g, nodes.data(), &n) == cudaSuccess, "cudaGraphGetNodes");
+  int64_t total = 0, ours = 0;
+  for (auto nd : nodes) {
+    cudaGraphNodeType t;
+    if (cudaGraphNodeGetType(nd, &t) != cudaSuccess || t != cudaGraphNodeTypeKernel) continue;
+    ++total;
+    cudaKernelNodeParams kp;
+    if (cudaGraphKernelNodeGetParams(nd, &kp) != cudaSuccess) continue;
+    const char* name = nullptr;
+    if (cudaFuncGetName(&name, kp.func) == cudaSuccess && name && std::strstr(name, "b200")) ++ours;
+  }
+  return {total, ours};
 }
 
 }  // namespace
@@ -177,6 +256,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_align", &moe_align);
   m.def("moe_gather", &moe_gather);
   m.def("moe_combine", &moe_combine);
+  m.def("gemm_grouped", &gemm_grouped);
+  m.def("num_sms", &num_sms);
+  m.def("graph_kernel_count", &graph_kernel_count);
+  m.def("fill_bytes", &fill_bytes);
   register_attn(m);
   register_comm(m);
 }

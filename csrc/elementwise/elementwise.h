@@ -14,8 +14,10 @@ int b200_kv_store(const void* kv, int f32, int64_t ld, int T, int L, int R, cons
 int b200_router(const float* logits, const float* bias, int T, int E, int G, int topk_group, int K, float scaling,
                 int renorm, float* w_out, int* id_out, cudaStream_t st);
 int b200_moe_align(const int* ids, const float* w, int T, int K, int first, int E, int* seg_start, int* seg_count,
-                   int* row_token, float* row_weight, int* pair_row, int* total_rows, cudaStream_t st);
-int b200_moe_gather(const uint8_t* xq, const uint8_t* xsf, const int* row_token, int rows_total, int Kd, uint8_t* dq,
+                   int* row_token, float* row_weight, int* pair_row, int* total_rows, int bn1, int* ttile1, int bn2,
+                   int* ttile2, cudaStream_t st);
+int b200_moe_gather(const uint8_t* xq, const uint8_t* xsf, const int* pair_row, int npairs, int K, int Kd, uint8_t* dq,
                     uint8_t* dsf, cudaStream_t st);
 int b200_moe_combine(const void* y, const int* pair_row, int T, int K, int D, const void* add, int add_f32, void* out,
                      int out_f32, cudaStream_t st);
+int b200_fill_bytes(void* p, int64_t nbytes, uint64_t seed, uint8_t and_mask, uint8_t or_mask, cudaStream_t st);

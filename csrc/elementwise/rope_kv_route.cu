@@ -180,7 +180,8 @@ __global__ void router_kernel(const float* logits, const float* bias, int T, int
 // One CTA; counts via shared-memory atomics.
 // ---------------------------------------------------------------------------
 __global__ void moe_align_kernel(const int* ids, const float* w, int T, int K, int first, int E, int* seg_start,
-                                 int* seg_count, int* row_token, float* row_weight, int* pair_row, int* total_rows) {
+                                 int* seg_count, int* row_token, float* row_weight, int* pair_row, int* total_rows,
+                                 int bn1, int* ttile1, int bn2, int* ttile2) {
   extern __shared__ int sh[];
   int* cnt = sh;          // [E]
   int* start = sh + E;    // [E]
@@ -195,11 +196,17 @@ __global__ void moe_align_kernel(const int* ids, const float* w, int T, int K, i
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    int acc = 0;
+    int acc = 0, a1 = 0, a2 = 0;
     for (int e = 0; e < E; ++e) {
       start[e] = acc;
       acc += (cnt[e] + 127) & ~127;
+      if (ttile1) ttile1[e] = a1;
+      if (ttile2) ttile2[e] = a2;
+      a1 += (cnt[e] + bn1 - 1) / bn1;
+      a2 += (cnt[e] + bn2 - 1) / bn2;
     }
+    if (ttile1) ttile1[E] = a1;
+    if (ttile2) ttile2[E] = a2;
     *total_rows = acc;
   }
   __syncthreads();
@@ -221,16 +228,17 @@ __global__ void moe_align_kernel(const int* ids, const float* w, int T, int K, i
   pdl_launch_dependents();
 }
 
-// Gather MXFP8 rows: dst row r <- src row row_token[r] (data + scale bytes).
-// grid (rows_total), block 128.  Rows not in any segment are skipped via
-// row_token < 0 (the caller initialises row_token to -1).
-__global__ void moe_gather_kernel(const uint8_t* xq, const uint8_t* xsf, const int* row_token, int rows_total, int Kd,
-                                  uint8_t* dq, uint8_t* dsf) {
-  const int r = blockIdx.x;
+// Gather MXFP8 rows for the local experts: for routed pair i = (t, j) with a
+// local expert, sorted row pair_row[i] <- token row t (data + scale bytes).
+// grid (T*K), block 128.
+__global__ void moe_gather_kernel(const uint8_t* xq, const uint8_t* xsf, const int* pair_row, int npairs, int K,
+                                  int Kd, uint8_t* dq, uint8_t* dsf) {
+  const int i = blockIdx.x;
   pdl_wait();
-  if (r >= rows_total) return;
-  const int t = row_token[r];
-  if (t < 0) return;
+  if (i >= npairs) return;
+  const int r = pair_row[i];
+  if (r < 0) return;
+  const int t = i / K;
   const uint4* s = reinterpret_cast<const uint4*>(xq + (int64_t)t * Kd);
   uint4* d = reinterpret_cast<uint4*>(dq + (int64_t)r * Kd);
   for (int i = threadIdx.x; i < Kd / 16; i += blockDim.x) d[i] = s[i];
@@ -306,16 +314,18 @@ int b200_router(const float* logits, const float* bias, int T, int E, int G, int
 }
 
 int b200_moe_align(const int* ids, const float* w, int T, int K, int first, int E, int* seg_start, int* seg_count,
-                   int* row_token, float* row_weight, int* pair_row, int* total_rows, cudaStream_t st) {
+                   int* row_token, float* row_weight, int* pair_row, int* total_rows, int bn1, int* ttile1, int bn2,
+                   int* ttile2, cudaStream_t st) {
   moe_align_kernel<<<1, 1024, 3 * E * sizeof(int), st>>>(ids, w, T, K, first, E, seg_start, seg_count, row_token,
-                                                         row_weight, pair_row, total_rows);
+                                                         row_weight, pair_row, total_rows, bn1 > 0 ? bn1 : 128, ttile1,
+                                                         bn2 > 0 ? bn2 : 128, ttile2);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
 
-int b200_moe_gather(const uint8_t* xq, const uint8_t* xsf, const int* row_token, int rows_total, int Kd, uint8_t* dq,
+int b200_moe_gather(const uint8_t* xq, const uint8_t* xsf, const int* pair_row, int npairs, int K, int Kd, uint8_t* dq,
                     uint8_t* dsf, cudaStream_t st) {
-  if (rows_total <= 0) return 0;
-  moe_gather_kernel<<<rows_total, 128, 0, st>>>(xq, xsf, row_token, rows_total, Kd, dq, dsf);
+  if (npairs <= 0) return 0;
+  moe_gather_kernel<<<npairs, 128, 0, st>>>(xq, xsf, pair_row, npairs, K, Kd, dq, dsf);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
 

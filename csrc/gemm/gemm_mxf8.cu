@@ -39,7 +39,8 @@ template <int BN, int EPI>
 struct Cfg {
   static constexpr int kA = (EPI == kEpiSwiglu) ? 2 : 1;         // A tiles per stage
   static constexpr int kBChunks = (BN + 127) / 128;               // SF chunks for B
-  static constexpr int kStageBytes = kA * kTileM * kTileK + BN * kTileK + kA * kSfChunk + kBChunks * kSfChunk;
+  static constexpr int kLoadBytes = kA * kTileM * kTileK + BN * kTileK + kA * kSfChunk + kBChunks * kSfChunk;
+  static constexpr int kStageBytes = kLoadBytes + kSfChunk;   // + a repack chunk for the activation scales
   static constexpr int kStages0 = (200 * 1024) / kStageBytes;
   static constexpr int kStages = kStages0 > 12 ? 12 : kStages0;
   static constexpr int kAccCols = kA * BN;
@@ -94,7 +95,8 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
   uint8_t* sB = sA + C::kStages * C::kA * kTileM * kTileK;               // [S][BN*128]
   uint8_t* sSFA = sB + C::kStages * BN * kTileK;                          // [S][kA][512]
   uint8_t* sSFB = sSFA + C::kStages * C::kA * kSfChunk;                   // [S][kBChunks][512]
-  uint64_t* full = reinterpret_cast<uint64_t*>(sSFB + C::kStages * C::kBChunks * kSfChunk);
+  uint8_t* sRep = sSFB + C::kStages * C::kBChunks * kSfChunk;                  // [S][512] repacked scales
+  uint64_t* full = reinterpret_cast<uint64_t*>(sRep + C::kStages * kSfChunk);
   uint64_t* empty = full + C::kStages;
   uint64_t* accbar = empty + C::kStages;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(accbar + 1);
@@ -119,7 +121,10 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
   const int kt0 = split * p.k_tiles_per_split;
   int nk = p.k / kTileK - kt0;
   if (nk > p.k_tiles_per_split) nk = p.k_tiles_per_split;
-  if (nk <= 0) return;
+  if (nk < 0) nk = 0;
+  // A cluster's CTAs must all reach its barriers: an empty split stays and
+  // contributes zeros.
+  if (nk == 0 && EPI != kEpiClusterSplit) return;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
@@ -152,7 +157,7 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
   if (warp == 0) {
     // ------------------------------ producer ------------------------------
     if (lane == 0) {
-      constexpr uint32_t bytes = C::kA * kTileM * kTileK + BN * kTileK + C::kA * kSfChunk + C::kBChunks * kSfChunk;
+      constexpr uint32_t bytes = C::kLoadBytes;
       for (int i = 0; i < nk; ++i) {
         const int s = i % C::kStages;
         if (i >= C::kStages) {
@@ -186,15 +191,34 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
       const int s = i % C::kStages;
       if (!mbar_wait(&full[s], (i / C::kStages) & 1, p.err)) { ok = false; break; }
       tc_fence_after();
+      // Token tiles of BN <= 128 rows may start at row o = b_row % 128 of a
+      // scale chunk: repack rows o..o+BN-1 into a tile-local chunk so the
+      // MMA reads the activation scales at the base TMEM column.
+      const int o = b_row & 127;
+      if (BN <= 128 && o != 0) {
+        const uint8_t* src = sSFB + (size_t)s * C::kBChunks * kSfChunk;
+        uint8_t* dst = sRep + (size_t)s * kSfChunk;
+        for (int j = lane; j < BN; j += 32) {
+          const int r = o + j;
+          *reinterpret_cast<uint32_t*>(dst + (j & 31) * 16 + (j >> 5) * 4) =
+              *reinterpret_cast<const uint32_t*>(src + (r & 31) * 16 + (r >> 5) * 4);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+      }
       if (lane == 0) {
         const uint32_t sf_a = tmem_sf + s * (C::kSfColsA + C::kSfColsB);
         const uint32_t sf_b = sf_a + C::kSfColsA;
         const uint8_t* sfa_src = sSFA + (size_t)s * C::kA * kSfChunk;
         for (int a = 0; a < C::kA; ++a)
           tmem_cp_32x128b_x4(sf_a + 4 * a, smem_desc(smem_u32(sfa_src + a * kSfChunk), 0, 128, 0));
-        for (int c = 0; c < C::kBChunks; ++c)
-          tmem_cp_32x128b_x4(sf_b + 4 * c,
-                             smem_desc(smem_u32(sSFB + ((size_t)s * C::kBChunks + c) * kSfChunk), 0, 128, 0));
+        if (BN <= 128 && o != 0) {
+          tmem_cp_32x128b_x4(sf_b, smem_desc(smem_u32(sRep + (size_t)s * kSfChunk), 0, 128, 0));
+        } else {
+          for (int c = 0; c < C::kBChunks; ++c)
+            tmem_cp_32x128b_x4(sf_b + 4 * c,
+                               smem_desc(smem_u32(sSFB + ((size_t)s * C::kBChunks + c) * kSfChunk), 0, 128, 0));
+        }
         const uint32_t a_base = smem_u32(sA + (size_t)s * C::kA * kTileM * kTileK);
         const uint32_t b_base = smem_u32(sB + (size_t)s * BN * kTileK);
         for (int kk = 0; kk < kTileK / 32; ++kk) {
@@ -203,11 +227,8 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
           for (int a = 0; a < C::kA; ++a) {
             const uint64_t adesc = desc_kmajor_sw128(a_base + a * kTileM * kTileK + kk * 32);
             const uint32_t idesc = idesc_mxf8(kTileM, BN, kk, kk);
-            // B scales: the tile's first row sits at row (b_row % 128) of its
-            // 128-row chunk, i.e. TMEM column (b_row % 128) / 32 (BN >= 32 or
-            // b_row % 128 == 0 keeps the lane index equal to the tile row).
             mma_mxf8(tmem_acc + a * BN, adesc, bdesc, idesc, (sf_a + 4 * a) | (uint32_t(kk) << 30),
-                     (sf_b + ((b_row & 127) >> 5)) | (uint32_t(kk) << 30), acc);
+                     sf_b | (uint32_t(kk) << 30), acc);
           }
         }
         mma_commit(&empty[s]);
@@ -227,7 +248,19 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
     if (ok) {
       const uint32_t lane_addr = tmem_acc + (uint32_t(sub * 32) << 16);
       const int tmax = rows - tile_t * BN;           // valid token columns in this tile
-      if (EPI == kEpiStoreBf16 || EPI == kEpiAtomicF32 || EPI == kEpiWeightedBf16) {
+      if (EPI == kEpiClusterSplit) {
+        // stage this split's partial tile: red[row][BN+1] over the (drained) A stages
+        float* red = reinterpret_cast<float*>(sA);
+        const int row = sub * 32 + lane;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          uint32_t r[16];
+          tmem_ld_x16(lane_addr + c0, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) red[row * (BN + 1) + c0 + j] = nk > 0 ? __uint_as_float(r[j]) : 0.f;
+        }
+      } else if (EPI == kEpiStoreBf16 || EPI == kEpiAtomicF32 || EPI == kEpiWeightedBf16) {
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 16) {
           uint32_t r[16];
@@ -284,6 +317,28 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (EPI == kEpiClusterSplit) {
+    // Every split of this output tile has staged its partial; CTA `rank`
+    // sums rows [rank*RPC, (rank+1)*RPC) of the tile across the cluster.
+    cluster_sync();
+    const int S = gridDim.z;
+    const uint32_t rank = cluster_ctarank();
+    const int rpc = kTileM / S;
+    const uint32_t red_local = smem_u32(sA);
+    const int tmax = rows - tile_t * BN;
+    for (int i = threadIdx.x; i < rpc * BN; i += kThreads) {
+      const int rr = rank * rpc + (i % rpc);
+      const int col = i / rpc;
+      if (col < tmax) {
+        const uint32_t off = (uint32_t)(rr * (BN + 1) + col) * 4u;
+        float acc = 0.f;
+        for (int q = 0; q < S; ++q) acc += ld_dsmem_f32(mapa_shared(red_local + off, q));
+        reinterpret_cast<__nv_bfloat16*>(p.out)[(int64_t)(b_row + col) * p.ldo + tile_n * kTileM + rr] =
+            __float2bfloat16(acc);
+      }
+    }
+    cluster_sync();
+  }
   if (warp == 0 && lane == 0) pdl_launch_dependents();
   if (warp == 1) {
     tc_fence_after();
@@ -362,11 +417,19 @@ static int launch_t(const GemmArgs& a, cudaStream_t st) {
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = C::kSmemBytes;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = a.pdl ? 1 : 0;
+  int nattr = 1;
+  if (EPI == kEpiClusterSplit) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = grid.z;
+    nattr = 2;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = nattr;
   cudaError_t err = cudaLaunchKernelEx(&cfg, kern, ma, mb, p);
   return err == cudaSuccess ? 0 : 1000 + int(err);
 }
@@ -396,6 +459,9 @@ int b200_gemm_mxf8(const GemmArgs* a, cudaStream_t st) {
     case kEpiAtomicF32: return g ? -10 : launch_bn<kEpiAtomicF32, false>(*a, st);
     case kEpiSwiglu: return g ? launch_bn<kEpiSwiglu, true>(*a, st) : launch_bn<kEpiSwiglu, false>(*a, st);
     case kEpiWeightedBf16: return g ? launch_bn<kEpiWeightedBf16, true>(*a, st) : -11;
+    case kEpiClusterSplit:
+      if (g || a->splits < 2 || a->splits > 8 || (128 % a->splits) != 0 || a->t > 128) return -13;
+      return launch_bn<kEpiClusterSplit, false>(*a, st);
   }
   return -12;
 }

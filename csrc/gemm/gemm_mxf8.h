@@ -8,6 +8,7 @@ enum GemmEpi : int {
   kEpiAtomicF32 = 1,     // out[row, n] += acc (fp32, split-K)
   kEpiSwiglu = 2,        // q_out/sf_out = mxfp8(silu(gate) * up)
   kEpiWeightedBf16 = 3,  // out[row, n] = bf16(acc * row_weight[row])  (grouped only)
+  kEpiClusterSplit = 4,  // split-K over a thread-block cluster, DSMEM reduction, bf16 out
 };
 
 struct GemmArgs {
@@ -39,3 +40,29 @@ struct GemmArgs {
 };
 
 int b200_gemm_mxf8(const GemmArgs* args, cudaStream_t stream);
+
+// Persistent grouped GEMM over the routed experts (see gemm_grouped.cu).
+struct GroupedArgs {
+  const uint8_t* w;        // e4m3 [E, nw, k]
+  const uint8_t* w_sf;
+  int64_t w_sf_estride;
+  const uint8_t* x;        // e4m3 sorted rows [x_rows, k]
+  const uint8_t* x_sf;
+  int64_t x_rows;
+  int nw, k, E, inter;
+  int bn;                  // token tile: 16/32/64 (swiglu), up to 128 (weighted)
+  const int* seg_start;
+  const int* seg_count;
+  const int* ttile_off;    // [E+1] prefix of ceil(count/bn)
+  int epi;                 // kEpiSwiglu or kEpiWeightedBf16
+  void* out;
+  int ldo;
+  uint8_t* q_out;
+  uint8_t* sf_out;
+  int ldq;
+  const float* row_weight;
+  uint32_t* err;
+  int num_ctas;
+  int pdl;
+};
+int b200_gemm_grouped(const GroupedArgs* args, cudaStream_t stream);

@@ -198,3 +198,69 @@ def test_mla_simt_matches_reference():
     got = cuda.mla_attention(q_abs.to(DEV), q_pe.to(DEV), cache.to(DEV), 0.7, fb, 0.06, ps)
     exp = ref.mla_attention(q_abs, q_pe, cache, 0.7, bt, torch.tensor(lens), q_seq, q_pos, 0.06, ps)
     assert rel_err(got.cpu(), exp) < 1e-2
+
+
+@pytest.mark.parametrize("H,lens,decode", [(16, [5, 40, 77], False), (16, [1000, 130, 2050, 64], True),
+                                           (64, [300, 1], True), (128, [700], True), (32, [129, 256], False)])
+def test_mla_tc_matches_reference(H, lens, decode):
+    from types import SimpleNamespace
+    from b200ds.ops import cuda, ref
+    B, L, R, ps = len(lens), 512, 64, 64
+    torch.manual_seed(0)
+    pages_per = [(n + ps - 1) // ps for n in lens]
+    bt = torch.zeros(B, max(pages_per) + 1, dtype=torch.int32)
+    perm = torch.randperm(sum(pages_per)) + 1
+    k = 0
+    for b in range(B):
+        for j in range(pages_per[b]):
+            bt[b, j] = int(perm[k])
+            k += 1
+    cache = (torch.randn((sum(pages_per) + 1) * ps, L + R) * 0.5).to(torch.float8_e4m3fn)
+    if decode:
+        q_seq = torch.arange(B, dtype=torch.int32)
+        q_pos = torch.tensor([n - 1 for n in lens], dtype=torch.int32)
+    else:
+        q_seq = torch.tensor([b for b in range(B) for _ in range(3)], dtype=torch.int32)
+        q_pos = torch.tensor([max(0, n - 3 + j) for n in lens for j in range(3)], dtype=torch.int32)
+    T = q_seq.numel()
+    q_abs = (torch.randn(T, H, L) * 0.3).to(torch.bfloat16)
+    q_pe = (torch.randn(T, H, R) * 0.3).to(torch.bfloat16)
+    fb = SimpleNamespace(block_table=bt.to(DEV), q_seq=q_seq.to(DEV), positions=q_pos.to(DEV),
+                         is_decode=decode, max_seq_len=max(lens))
+    got = cuda.mla_attention(q_abs.to(DEV), q_pe.to(DEV), cache.to(DEV), 0.7, fb, 0.0625, ps)
+    exp = ref.mla_attention(q_abs, q_pe, cache, 0.7, bt, torch.tensor(lens), q_seq, q_pos, 0.0625, ps)
+    err = rel_err(got.cpu(), exp)
+    assert err < 3e-2, err
+
+
+@pytest.mark.parametrize("T,N,K,S", [(1, 2176, 7168, 8), (64, 7168, 2048, 2), (16, 384, 1536, 4), (100, 256, 4096, 8),
+                                     (64, 512, 384, 2)])
+def test_gemm_cluster_splitk(T, N, K, S):
+    from b200ds.ops import QAct, cuda, ref
+    a = _mx(torch.randn(T, K, device=DEV))
+    wq = _mx(torch.randn(N, K, device=DEV) * 0.05)
+    out = torch.empty(T, N, dtype=torch.bfloat16, device=DEV)
+    cuda._gemm_raw(QAct(a.data, a.sf), wq, out, 4, splits=S)
+    exp = ref.gemm_mxfp8(a.data, a.sf, wq.data, wq.sf)
+    assert rel_err(out, exp) < 5e-3
+
+
+@pytest.mark.parametrize("T,hot", [(64, 8), (40, 2)])
+def test_moe_experts_skewed_routing(T, hot):
+    """Every token routed to the same few experts: several 16-row token tiles
+    per expert (tiles at 16-row offsets inside a scale-factor chunk)."""
+    from b200ds.ops import ExpertWeights, QAct, cuda
+    from b200ds.ops.quant import MXFP8Tensor, dequant_mxfp8
+    import b200ds.ops as ops
+    H, I, E, K = 1024, 256, 32, 8 if hot == 8 else 2
+    w13 = [_mx(torch.randn(2 * I, H, device=DEV) * 0.05) for _ in range(E)]
+    w2 = [_mx(torch.randn(H, I, device=DEV) * 0.05) for _ in range(E)]
+    ex = ExpertWeights(0, E, MXFP8Tensor(torch.stack([w.data for w in w13]), torch.stack([w.sf for w in w13])),
+                       MXFP8Tensor(torch.stack([w.data for w in w2]), torch.stack([w.sf for w in w2])), I)
+    a = _mx(torch.randn(T, H, device=DEV))
+    ids = torch.arange(K, device=DEV, dtype=torch.int32).repeat(T, 1) * 3
+    wts = torch.rand(T, K, device=DEV)
+    got = cuda.moe_experts(QAct(a.data, a.sf), wts, ids, ex, torch.float32, n_experts_total=256)
+    exc = ExpertWeights(0, E, MXFP8Tensor(ex.w13.data.cpu(), ex.w13.sf.cpu()), MXFP8Tensor(ex.w2.data.cpu(), ex.w2.sf.cpu()), I)
+    exp = ops.moe_experts(dequant_mxfp8(a.data, a.sf).cpu(), wts.cpu(), ids.cpu(), exc, torch.float32)
+    assert rel_err(got.cpu(), exp) < 3e-2, rel_err(got.cpu(), exp)
