@@ -28,3 +28,26 @@ struct MlaTcArgs {
 };
 int b200_mla_q_quant(const void* q_abs, const void* q_pe, int TH, uint8_t* q8, float* qs, cudaStream_t st);
 int b200_mla_tc(const MlaTcArgs* args, cudaStream_t st);
+
+// ---------------------------------------------------------------------------
+// Allocation-free MLA decode (absorbed MLA over the paged e4m3 latent cache,
+// split-KV with merge), for callers that cannot allocate device memory: its
+// scratch lives in fixed device arrays inside the library (about 10.8 MB per
+// GPU, held until exit; limits T*H <= 4096 and nsplit*T*H <= 4096).  Inputs:
+// q_abs bf16 [T,H,512], q_pe bf16 [T,H,64], kv_cache e4m3 [cache_rows,576],
+// int32 block_table [*, bt_stride] / q_seq [T] / q_pos [T]; output bf16
+// [T,H,512].  Returns 0 or a B200_NOALLOC_ERR_* code (see
+// b200_mla_decode_noalloc_error).  Calls share the scratch, so calls that
+// overlap on the GPU race; the first call on a device sets up the scratch
+// addresses and should come before any stream capture.
+// This entry point has no counterpart in the reference.
+// ---------------------------------------------------------------------------
+#define B200_NOALLOC_ERR_BAD_ARG (-1)
+#define B200_NOALLOC_ERR_TOO_LARGE (-2)
+#define B200_NOALLOC_ERR_SETUP (-3)
+#define B200_NOALLOC_ERR_LAUNCH (-4)
+extern "C" int b200_mla_decode_noalloc(const void* q_abs, const void* q_pe, int T, int H, const void* kv_cache,
+                                       long long cache_rows, const int* block_table, int bt_stride, const int* q_seq,
+                                       const int* q_pos, int page_size, float sm_scale, float kv_scale, int nsplit,
+                                       void* out, cudaStream_t stream);
+extern "C" const char* b200_mla_decode_noalloc_error(int code);

@@ -503,3 +503,107 @@ int b200_mla_tc(const MlaTcArgs* a, cudaStream_t st) {
   if (a->H % 16 == 0) return launch<16>(*a, st);
   return -6;
 }
+
+// ===========================================================================
+// Allocation-free MLA decode entry point.
+//
+// For callers that must not allocate device memory themselves: a host
+// runtime that has already handed all of HBM to its own pool (weights + KV
+// cache reserved up front), or one that cannot afford the device-wide
+// synchronisation that cudaMalloc / cudaFree may cause in the middle of
+// serving.  The caller passes inputs and the output; the kernel's scratch
+// (quantised queries, per-split partial outputs and log-sum-exps) lives in
+// the fixed device arrays below.
+//
+// Limits: T * H <= kNoAllocMaxRows query rows and nsplit * T * H <=
+// kNoAllocMaxPartRows split partials; larger requests are rejected with
+// B200_NOALLOC_ERR_TOO_LARGE.  The arrays total about 10.8 MB and every GPU
+// that loads this library keeps them until the process exits.  All calls
+// share them: two calls whose kernels overlap on the GPU (different streams,
+// or different host threads) race on the scratch and give wrong results.
+// Nothing in the scratch needs to start at zero: each call writes every
+// element it later reads.  The first call on a device looks up the arrays'
+// device addresses (cudaGetSymbolAddress) with that device current; make
+// that first call before any stream capture.
+// ===========================================================================
+#include <mutex>
+
+namespace {
+constexpr int kNoAllocMaxRows = 4096;                  // T * H
+constexpr int kNoAllocMaxPartRows = 4096;              // nsplit * T * H
+static __device__ __align__(256) uint8_t g_noalloc_q8[kNoAllocMaxRows * 576];
+static __device__ __align__(256) float g_noalloc_qscale[kNoAllocMaxRows];
+static __device__ __align__(256) float g_noalloc_part_o[kNoAllocMaxPartRows * 512];
+static __device__ __align__(256) float g_noalloc_part_lse[kNoAllocMaxPartRows];
+
+constexpr int kMaxDevices = 64;
+struct NoAllocScratch {
+  bool ready = false;
+  uint8_t* q8 = nullptr;
+  float* qscale = nullptr;
+  float* part_o = nullptr;
+  float* part_lse = nullptr;
+};
+NoAllocScratch g_scratch[kMaxDevices];
+std::mutex g_scratch_mu;
+
+int noalloc_setup(int dev) {
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  NoAllocScratch& s = g_scratch[dev];
+  if (s.ready) return 0;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&s.q8), g_noalloc_q8) != cudaSuccess) return -1;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&s.qscale), g_noalloc_qscale) != cudaSuccess) return -1;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&s.part_o), g_noalloc_part_o) != cudaSuccess) return -1;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&s.part_lse), g_noalloc_part_lse) != cudaSuccess) return -1;
+  s.ready = true;
+  return 0;
+}
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) int b200_mla_decode_noalloc(
+    const void* q_abs, const void* q_pe, int T, int H, const void* kv_cache, long long cache_rows,
+    const int* block_table, int bt_stride, const int* q_seq, const int* q_pos, int page_size, float sm_scale,
+    float kv_scale, int nsplit, void* out, cudaStream_t stream) {
+  if (T <= 0 || H <= 0 || nsplit < 1 || nsplit > 16 || page_size != b200::mla::kPage || (H % 16) != 0 ||
+      !q_abs || !q_pe || !kv_cache || !block_table || !q_seq || !q_pos || !out)
+    return B200_NOALLOC_ERR_BAD_ARG;
+  if ((long long)T * H > kNoAllocMaxRows || (long long)nsplit * T * H > kNoAllocMaxPartRows)
+    return B200_NOALLOC_ERR_TOO_LARGE;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return B200_NOALLOC_ERR_SETUP;
+  if (noalloc_setup(dev) != 0) return B200_NOALLOC_ERR_SETUP;
+  const NoAllocScratch& s = g_scratch[dev];
+  if (b200_mla_q_quant(q_abs, q_pe, T * H, s.q8, s.qscale, stream) != 0) return B200_NOALLOC_ERR_LAUNCH;
+  MlaTcArgs a{};
+  a.q8 = s.q8;
+  a.q_scale = s.qscale;
+  a.cache = reinterpret_cast<const uint8_t*>(kv_cache);
+  a.cache_rows = cache_rows;
+  a.block_table = block_table;
+  a.bt_stride = bt_stride;
+  a.q_seq = q_seq;
+  a.q_pos = q_pos;
+  a.T = T;
+  a.H = H;
+  a.page_size = page_size;
+  a.nsplit = nsplit;
+  a.sm_scale = sm_scale;
+  a.kv_scale = kv_scale;
+  a.out = out;
+  a.part_o = s.part_o;
+  a.part_lse = s.part_lse;
+  return b200_mla_tc(&a, stream) == 0 ? 0 : B200_NOALLOC_ERR_LAUNCH;
+}
+
+extern "C" __attribute__((visibility("default"))) const char* b200_mla_decode_noalloc_error(int code) {
+  switch (code) {
+    case 0: return "ok";
+    case B200_NOALLOC_ERR_BAD_ARG:
+      return "bad argument (null pointer, T/H <= 0, H not a multiple of 16, nsplit outside 1..16, page size != 64)";
+    case B200_NOALLOC_ERR_TOO_LARGE:
+      return "request exceeds the static scratch: need T*H <= 4096 and nsplit*T*H <= 4096";
+    case B200_NOALLOC_ERR_SETUP: return "could not look up the scratch arrays' device addresses";
+    case B200_NOALLOC_ERR_LAUNCH: return "kernel launch failed";
+  }
+  return "unknown error";
+}
