@@ -112,6 +112,10 @@ class DeepseekModel:
         self.ix_cache: List[torch.Tensor] = []
         self.ix_scale: List[torch.Tensor] = []
         self.page_size = ecfg.page_size
+        if (self.device.type == "cuda" and ps.tp_size > 1 and ecfg.comm_impl == "fused"
+                and getattr(ps, "fused_ar", None) is None):
+            from ..parallel.symm import FusedAllReduce
+            ps.fused_ar = FusedAllReduce(ps, cfg.hidden_size, max_tokens=max(ecfg.max_num_seqs, 256))
 
     # ------------------------------------------------------------------
     def allocate_kv(self, num_pages: int):

@@ -83,6 +83,15 @@ def add_rmsnorm_act(a: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, ep
 
 
 def allreduce_add_rmsnorm(a, residual, w, eps, ps, next_linear=None):
+    """TP all-reduce + residual add + RMSNorm (+ MXFP8 quant): one fused
+    NVLink kernel pair when the symmetric workspace is set up and the step
+    fits it, else NCCL followed by the fused add+norm kernel."""
+    far = getattr(ps, "fused_ar", None)
+    if far is not None and far.supports(a.shape[0]):
+        quantized = next_linear is not None and getattr(next_linear, "quantized", False)
+        if residual.dtype != torch.float32:
+            residual = residual.float()
+        return far.allreduce_add_rmsnorm(a, residual, w, eps, quantized)
     from . import comm
     a = comm.all_reduce(a, ps)
     return add_rmsnorm_act(a, residual, w, eps, next_linear)

@@ -43,6 +43,7 @@ class ParallelState:
     dp_group: Optional[object] = None
     cpu_group: Optional[object] = None
     device: torch.device = torch.device("cpu")
+    fused_ar: Optional[object] = None       # parallel.symm.FusedAllReduce when enabled
 
     @property
     def distributed(self) -> bool:

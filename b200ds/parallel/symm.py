@@ -1,0 +1,71 @@
+"""Symmetric (peer-mapped) workspaces for the fused NVLink collectives.
+
+`FusedAllReduce` owns one torch symmetric-memory buffer per tensor-parallel
+group: arrival counters plus two parities of per-source receive slots
+[world][max_tokens][hidden] bf16.  Its `allreduce_add_rmsnorm` pushes the
+local partial into every rank's slot (P2P stores over NVLink) and then runs
+the reduce + residual + RMSNorm + MXFP8 kernel; steps with more tokens than
+`max_tokens` (long prefill chunks) use NCCL instead.
+
+Reference parity: symmetric-memory rendezvous of the EPA / LGP buffers
+(epa.py:994-1010, lgp.py:272-291).
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+
+class FusedAllReduce:
+    def __init__(self, ps, hidden: int, max_tokens: int = 256, push_ctas: int = 32):
+        import torch.distributed._symmetric_memory as symm_mem
+        from .. import _C
+        self.ps = ps
+        self.hidden = hidden
+        self.max_tokens = max_tokens
+        self.push_ctas = push_ctas
+        self.world = ps.tp_size
+        self.rank = ps.tp_rank
+        dev = ps.device
+        group = ps.tp_group
+        name = group.group_name
+        if hasattr(symm_mem, "enable_symm_mem_for_group") and not symm_mem.is_symm_mem_enabled_for_group(name):
+            symm_mem.enable_symm_mem_for_group(name)
+        nbytes = int(_C.ar_buffer_size(self.world, max_tokens, hidden))
+        self.buf = symm_mem.empty(nbytes, dtype=torch.uint8, device=dev)
+        self.buf.zero_()
+        self.hdl = symm_mem.rendezvous(self.buf, name)
+        self.bases = [int(p) for p in self.hdl.buffer_ptrs]
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.ticket = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=group)
+
+    def supports(self, T: int) -> bool:
+        return 0 < T <= self.max_tokens
+
+    def allreduce_add_rmsnorm(self, a: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float,
+                              quantize: bool, keep_bf16: bool = True):
+        """residual += all_reduce(a); returns (normalized act, residual)."""
+        from .. import _C
+        from ..ops.cuda import alloc_qact
+        T, H = a.shape
+        x = a if (a.dtype == torch.bfloat16 and a.is_contiguous()) else a.to(torch.bfloat16).contiguous()
+        _C.ar_push(x, self.bases, self.rank, self.max_tokens, self.epoch, self.push_ctas)
+        y = torch.empty(T, H, dtype=torch.bfloat16, device=a.device) if (keep_bf16 or not quantize) else None
+        qa = alloc_qact(T, H, a.device) if quantize else None
+        _C.ar_reduce_norm(T, H, self.bases, self.rank, self.max_tokens, self.epoch, self.ticket, self.push_ctas,
+                          residual, w, eps, y, qa.q if qa else None, qa.sf if qa else None, self.err)
+        if qa is not None:
+            qa.hf = y
+            return qa, residual
+        return y, residual
+
+    def check(self) -> None:
+        """Raise if a bounded wait inside the kernels timed out."""
+        e = int(self.err.item())
+        if e:
+            raise RuntimeError(f"fused all-reduce: peer wait timed out (code {e})")

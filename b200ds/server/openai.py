@@ -1,0 +1,284 @@
+"""OpenAI-compatible HTTP server.
+
+Endpoints: POST /v1/completions, POST /v1/chat/completions (both with
+``stream: true`` server-sent events), GET /v1/models, GET /health,
+GET /metrics (Prometheus text).
+
+One engine thread owns the Engine and runs `step()` whenever requests are
+pending; HTTP handlers enqueue requests and await their tokens through
+per-request asyncio queues.  In a multi-GPU job rank 0 serves HTTP and, each
+step, broadcasts newly admitted requests to the other ranks over the gloo
+control group (`follower_loop` on ranks > 0), so every rank schedules the same
+batches.
+
+    python -m b200ds.server.openai --model deepseek-v3-671b --port 8000
+    torchrun --nproc-per-node 8 -m b200ds.server.openai --model <ckpt dir>
+
+Reference parity: the reference serves through SGLang's OpenAI server
+(absent); request metrics mirror its TTFT / TPOT reporting (fg.py:68-73).
+"""
+
+
+import argparse
+import asyncio
+import json
+import queue
+import threading
+import time
+import uuid
+from typing import Dict, List, Optional
+
+from ..engine.request import SamplingParams
+
+
+class EngineWorker:
+    """Runs Engine.step() on a background thread; thread-safe submission."""
+
+    def __init__(self, engine, tokenizer, ps=None):
+        self.engine = engine
+        self.tok = tokenizer
+        self.ps = ps
+        self.inbox: "queue.Queue" = queue.Queue()
+        self.subs: Dict[int, tuple] = {}     # rid -> (loop, asyncio.Queue, emitted count)
+        self._stop = threading.Event()
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.metrics = _Metrics()
+
+    def start(self):
+        self.t.start()
+        return self
+
+    def stop(self):
+        self._stop.set()
+        self.t.join(timeout=10)
+
+    def submit(self, prompt_ids: List[int], params: SamplingParams, loop, q) -> None:
+        self.inbox.put((prompt_ids, params, loop, q))
+
+    def _admit(self) -> List[tuple]:
+        new = []
+        while True:
+            try:
+                new.append(self.inbox.get_nowait())
+            except queue.Empty:
+                break
+        return new
+
+    def _run(self):
+        eng = self.engine
+        while not self._stop.is_set():
+            new = self._admit()
+            if self.ps is not None and self.ps.world_size > 1:
+                _broadcast_requests(self.ps, [(p, sp.__dict__) for p, sp, _, _ in new])
+            for prompt, params, loop, q in new:
+                r = eng.add_request(prompt, params)
+                self.subs[r.rid] = (loop, q, 0, r)
+                self.metrics.requests += 1
+            if not eng.sched.has_work:
+                time.sleep(0.002)
+                continue
+            t0 = time.perf_counter()
+            done = eng.step()
+            self.metrics.step_time.append(time.perf_counter() - t0)
+            for rid, (loop, q, sent, r) in list(self.subs.items()):
+                if len(r.output) > sent:
+                    new_toks = r.output[sent:]
+                    self.subs[rid] = (loop, q, len(r.output), r)
+                    loop.call_soon_threadsafe(q.put_nowait, ("tokens", new_toks))
+                if r.finished:
+                    loop.call_soon_threadsafe(q.put_nowait, ("done", r.finish_reason))
+                    self.metrics.finish(r)
+                    del self.subs[rid]
+
+
+def _broadcast_requests(ps, reqs):
+    import torch.distributed as dist
+    obj = [reqs]
+    dist.broadcast_object_list(obj, src=0, group=ps.cpu_group)
+    return obj[0]
+
+
+def follower_loop(engine, ps) -> None:
+    """Ranks > 0: mirror rank 0's admissions and step in lockstep."""
+    while True:
+        reqs = _broadcast_requests(ps, None)
+        for prompt, spd in reqs:
+            engine.add_request(prompt, SamplingParams(**spd))
+        if engine.sched.has_work:
+            engine.step()
+
+
+class _Metrics:
+    def __init__(self):
+        self.requests = 0
+        self.completed = 0
+        self.prompt_tokens = 0
+        self.gen_tokens = 0
+        self.ttft: List[float] = []
+        self.tpot: List[float] = []
+        self.step_time: List[float] = []
+
+    def finish(self, r):
+        self.completed += 1
+        self.prompt_tokens += len(r.prompt)
+        self.gen_tokens += len(r.output)
+        if r.t_first is not None:
+            self.ttft.append(r.t_first - r.t_arrive)
+        if r.t_done is not None and len(r.output) > 1:
+            self.tpot.append((r.t_done - r.t_first) / (len(r.output) - 1))
+
+    def prometheus(self) -> str:
+        def q(xs, p):
+            if not xs:
+                return 0.0
+            s = sorted(xs)
+            return s[min(len(s) - 1, int(p * len(s)))]
+        lines = [
+            f"b200ds_requests_total {self.requests}",
+            f"b200ds_requests_completed_total {self.completed}",
+            f"b200ds_prompt_tokens_total {self.prompt_tokens}",
+            f"b200ds_generation_tokens_total {self.gen_tokens}",
+            f'b200ds_ttft_seconds{{quantile="0.5"}} {q(self.ttft, 0.5)}',
+            f'b200ds_ttft_seconds{{quantile="0.99"}} {q(self.ttft, 0.99)}',
+            f'b200ds_tpot_seconds{{quantile="0.5"}} {q(self.tpot, 0.5)}',
+            f'b200ds_tpot_seconds{{quantile="0.99"}} {q(self.tpot, 0.99)}',
+            f'b200ds_step_seconds{{quantile="0.5"}} {q(self.step_time[-1000:], 0.5)}',
+        ]
+        return "\n".join(lines) + "\n"
+
+
+def _params(body: dict, default_max: int = 16) -> SamplingParams:
+    stop_ids = body.get("stop_token_ids") or []
+    return SamplingParams(
+        max_tokens=int(body.get("max_tokens") or default_max),
+        temperature=float(body.get("temperature", 1.0) if body.get("temperature") is not None else 1.0),
+        top_p=float(body.get("top_p", 1.0) or 1.0),
+        top_k=int(body.get("top_k", 0) or 0),
+        seed=body.get("seed"),
+        ignore_eos=bool(body.get("ignore_eos", False)),
+        stop_token_ids=list(stop_ids),
+    )
+
+
+def create_app(worker: EngineWorker, model_name: str = "b200ds"):
+    from fastapi import FastAPI, HTTPException, Request
+    from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
+
+    app = FastAPI(title="b200ds")
+    tok = worker.tok
+
+    async def _run(prompt_ids, params):
+        loop = asyncio.get_running_loop()
+        q: asyncio.Queue = asyncio.Queue()
+        worker.submit(prompt_ids, params, loop, q)
+        return q
+
+    def _prompt_ids(body, chat: bool):
+        if chat:
+            msgs = body.get("messages")
+            if not isinstance(msgs, list):
+                raise HTTPException(400, "messages must be a list")
+            text = tok.apply_chat_template(msgs)
+            return tok.encode(text)
+        p = body.get("prompt")
+        if isinstance(p, list) and all(isinstance(i, int) for i in p):
+            return p
+        if isinstance(p, list) and len(p) == 1 and isinstance(p[0], str):
+            p = p[0]
+        if not isinstance(p, str):
+            raise HTTPException(400, "prompt must be a string or a list of token ids")
+        return tok.encode(p)
+
+    async def _handle(request: Request, chat: bool):
+        body = await request.json()
+        ids = _prompt_ids(body, chat)
+        params = _params(body)
+        rid = f"{'chatcmpl' if chat else 'cmpl'}-{uuid.uuid4().hex[:16]}"
+        created = int(time.time())
+        q = await _run(ids, params)
+        obj = "chat.completion" if chat else "text_completion"
+        if body.get("stream"):
+            async def gen():
+                while True:
+                    kind, val = await q.get()
+                    if kind == "tokens":
+                        text = tok.decode(val)
+                        choice = ({"index": 0, "delta": {"content": text}, "finish_reason": None} if chat
+                                  else {"index": 0, "text": text, "token_ids": val, "finish_reason": None})
+                        yield f"data: {json.dumps({'id': rid, 'object': obj + '.chunk', 'created': created, 'model': model_name, 'choices': [choice]})}\n\n"
+                    else:
+                        choice = ({"index": 0, "delta": {}, "finish_reason": val} if chat
+                                  else {"index": 0, "text": "", "finish_reason": val})
+                        yield f"data: {json.dumps({'id': rid, 'object': obj + '.chunk', 'created': created, 'model': model_name, 'choices': [choice]})}\n\n"
+                        yield "data: [DONE]\n\n"
+                        return
+            return StreamingResponse(gen(), media_type="text/event-stream")
+        out: List[int] = []
+        reason = "length"
+        while True:
+            kind, val = await q.get()
+            if kind == "tokens":
+                out.extend(val)
+            else:
+                reason = val
+                break
+        text = tok.decode(out)
+        choice = ({"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": reason} if chat
+                  else {"index": 0, "text": text, "token_ids": out, "finish_reason": reason})
+        return JSONResponse({"id": rid, "object": obj, "created": created, "model": model_name, "choices": [choice],
+                             "usage": {"prompt_tokens": len(ids), "completion_tokens": len(out),
+                                       "total_tokens": len(ids) + len(out)}})
+
+    @app.post("/v1/completions")
+    async def completions(request: Request):
+        return await _handle(request, chat=False)
+
+    @app.post("/v1/chat/completions")
+    async def chat(request: Request):
+        return await _handle(request, chat=True)
+
+    @app.get("/v1/models")
+    async def models():
+        return {"object": "list", "data": [{"id": model_name, "object": "model", "owned_by": "b200ds"}]}
+
+    @app.get("/health")
+    async def health():
+        return {"status": "ok"}
+
+    @app.get("/metrics")
+    async def metrics():
+        return PlainTextResponse(worker.metrics.prometheus())
+
+    return app
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model", default="tiny", help="preset name or HF checkpoint directory")
+    ap.add_argument("--weights", default="random")
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=8000)
+    ap.add_argument("--max-num-seqs", type=int, default=256)
+    ap.add_argument("--no-cuda-graphs", action="store_true")
+    args = ap.parse_args(argv)
+    import uvicorn
+    from .. import load_engine
+    from ..config import EngineConfig
+    from ..engine.tokenizer import load_tokenizer
+    from ..parallel.state import init_parallel
+    ps = init_parallel()
+    ecfg = EngineConfig(tp_size=ps.tp_size, ep_size=ps.ep_size, max_num_seqs=args.max_num_seqs,
+                        cuda_graphs=not args.no_cuda_graphs)
+    eng = load_engine(args.model, weights=args.weights, ecfg=ecfg)
+    tok = load_tokenizer(args.model)
+    eng.tokenizer = tok
+    eng.eos = getattr(tok, "eos_token_id", None)
+    if ps.rank != 0:
+        follower_loop(eng, ps)
+        return
+    worker = EngineWorker(eng, tok, ps).start()
+    uvicorn.run(create_app(worker, model_name=str(args.model)), host=args.host, port=args.port, log_level="warning")
+
+
+if __name__ == "__main__":
+    main()

@@ -244,9 +244,12 @@ def main():
         }
         print(json.dumps(out), flush=True)
     eng.graphs.release()
+    torch.cuda.synchronize()
     if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+        try:
+            dist.destroy_process_group()
+        except Exception as e:  # the result line is already out
+            log(f"process-group teardown: {e}")
 
 
 def count_launches(gr) -> int:

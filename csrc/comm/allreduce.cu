@@ -1,0 +1,233 @@
+// Fused tensor-parallel all-reduce + residual add + RMSNorm + MXFP8 quant
+// over NVLink peer memory (one process per GPU, buffers from torch symmetric
+// memory).
+//
+// Symmetric buffer layout (identical on every rank, bytes from its base):
+//   [0, 256)                     uint32 arrival counters cnt[2][kMaxRanks]
+//   [kRecvOff, ...)              bf16 recv[2][world][max_t][hidden]
+// Two parities alternate between consecutive all-reduces (parity = epoch & 1,
+// epoch a device counter every rank advances in the same order), so a rank
+// never overwrites a slot a slower peer is still reading.
+//
+//   push (one kernel, or a GEMM / MoE-combine epilogue): rank r P2P-stores its
+//        partial rows into recv[p][r] of every rank, then each CTA publishes
+//        with a system-scope fence + one atomic increment of cnt[p][r] on
+//        every rank.
+//   reduce: each CTA waits (bounded by %globaltimer) until cnt[p][q] == the
+//        pushers' CTA count for all q, sums recv[p][0..W) in rank order (so
+//        every rank produces bitwise identical rows), adds the fp32 residual
+//        in place, RMSNorm, and writes bf16 and/or MXFP8 outputs.  The last
+//        CTA (ticket) zeroes cnt[p][*] and advances the epoch.
+//
+// Ordering argument for slot reuse: rank r's push at epoch e+2 is stream-
+// ordered after its reduce at e+1, which waited for every peer's push at
+// e+1, which each peer issued after finishing its own reduce at e.
+//
+// Reference parity: the reference's FIN push plane (fin.py:384, 16-byte
+// relaxed stores + Lamport markers, unbounded polls at fin.py:459-471) and
+// EPA epilogue push (epa.py:795, epa_gemm.py:1849-1890); here every poll is
+// bounded and reports an error code instead of hanging.
+#include "../common/ptx.cuh"
+#include "comm.h"
+
+namespace b200 {
+namespace comm {
+
+constexpr int kThreads = 256;
+constexpr int kMaxIt = 8;     // hidden <= 256 * 8 * 8 = 16384
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_sys_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int64_t sf_off(int row, int kblock, int kb_total) {
+  const int rb = row >> 7, r = row & 127, kc = kblock >> 2, c = kblock & 3;
+  return ((int64_t)(rb * (kb_total >> 2) + kc) << 9) + ((r & 31) << 4) + ((r >> 5) << 2) + c;
+}
+
+__device__ __forceinline__ uint32_t* counters(uint8_t* base, int parity) {
+  return reinterpret_cast<uint32_t*>(base) + parity * kArMaxRanks;
+}
+__device__ __forceinline__ __nv_bfloat16* recv_slot(uint8_t* base, int parity, int src, int world, int max_t,
+                                                    int hidden) {
+  return reinterpret_cast<__nv_bfloat16*>(base + kArRecvOff) +
+         ((int64_t)(parity * world + src) * max_t) * hidden;
+}
+
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads) ar_push_kernel(const __nv_bfloat16* __restrict__ x, int T, int hidden,
+                                                           ArPeers peers, const uint32_t* epoch) {
+  pdl_wait();
+  const int p = (*epoch) & 1;
+  const int64_t n16 = (int64_t)T * hidden / 8;       // 16-byte vectors
+  const int64_t per = (n16 + gridDim.x - 1) / gridDim.x;
+  const int64_t v0 = blockIdx.x * per;
+  const int64_t v1 = min(n16, v0 + per);
+  const uint4* src = reinterpret_cast<const uint4*>(x);
+  for (int q = 0; q < peers.world; ++q) {
+    uint4* dst = reinterpret_cast<uint4*>(recv_slot(peers.base[q], p, peers.rank, peers.world, peers.max_t, hidden));
+    for (int64_t v = v0 + threadIdx.x; v < v1; v += blockDim.x) dst[v] = src[v];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int q = 0; q < peers.world; ++q) red_release_sys_add(counters(peers.base[q], p) + peers.rank, 1u);
+  }
+}
+
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads) ar_reduce_norm_kernel(
+    int T, int hidden, ArPeers peers, uint32_t* epoch, uint32_t* ticket, uint32_t expected, float* residual,
+    const float* __restrict__ w, float eps, __nv_bfloat16* y, uint8_t* q, uint8_t* sf, uint32_t* err) {
+  __shared__ float red[32];
+  __shared__ int ok_s;
+  pdl_wait();
+  const int p = (*epoch) & 1;
+  uint8_t* mine = peers.base[peers.rank];
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const uint32_t* cnt = counters(mine, p);
+    const uint64_t t0 = globaltimer_ns();
+    for (int src = 0; src < peers.world && ok; ++src) {
+      while (ld_acquire_sys(cnt + src) < expected) {
+        if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+          atomicExch(err, kErrPeerTimeout);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    ok_s = ok;
+  }
+  __syncthreads();
+  const int row = blockIdx.x;
+  const int units = hidden >> 3;
+  if (ok_s && row < T) {
+    float v[kMaxIt][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int it = 0; it < kMaxIt; ++it) {
+      const int u = it * kThreads + threadIdx.x;
+      if (u < units) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[it][i] = 0.f;
+        for (int src = 0; src < peers.world; ++src) {
+          const __nv_bfloat16* s = recv_slot(mine, p, src, peers.world, peers.max_t, hidden) + (int64_t)row * hidden;
+          const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(s + u * 8));
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h[i]);
+            v[it][2 * i] += f.x;
+            v[it][2 * i + 1] += f.y;
+          }
+        }
+        float* rp = residual + (int64_t)row * hidden + u * 8;
+        const float4 r0 = *reinterpret_cast<const float4*>(rp);
+        const float4 r1 = *reinterpret_cast<const float4*>(rp + 4);
+        v[it][0] += r0.x; v[it][1] += r0.y; v[it][2] += r0.z; v[it][3] += r0.w;
+        v[it][4] += r1.x; v[it][5] += r1.y; v[it][6] += r1.z; v[it][7] += r1.w;
+        *reinterpret_cast<float4*>(rp) = make_float4(v[it][0], v[it][1], v[it][2], v[it][3]);
+        *reinterpret_cast<float4*>(rp + 4) = make_float4(v[it][4], v[it][5], v[it][6], v[it][7]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss += v[it][i] * v[it][i];
+      }
+    }
+    // block reduction of the sum of squares
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float s2 = threadIdx.x < (kThreads >> 5) ? red[threadIdx.x] : 0.f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+      if (threadIdx.x == 0) red[0] = s2;
+    }
+    __syncthreads();
+    const float rs = rsqrtf(red[0] / float(hidden) + eps);
+    const int kb_total = hidden >> 5;
+#pragma unroll
+    for (int it = 0; it < kMaxIt; ++it) {
+      if (it * kThreads >= units) break;
+      const int u = it * kThreads + threadIdx.x;
+      const bool valid = u < units;
+      float o[8];
+      if (valid) {
+        const float4 w0 = *reinterpret_cast<const float4*>(w + u * 8);
+        const float4 w1 = *reinterpret_cast<const float4*>(w + u * 8 + 4);
+        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = v[it][i] * rs * wv[i];
+        if (y) {
+          uint4 outv;
+          __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&outv);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
+          *reinterpret_cast<uint4*>(y + (int64_t)row * hidden + u * 8) = outv;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = 0.f;
+      }
+      if (q) {
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(o[i]));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        const int e = ceil_log2_bits(amax * (1.0f / 448.0f));
+        const float inv = exp2_int(-e);
+        uint2 packed;
+        uint16_t* o16 = reinterpret_cast<uint16_t*>(&packed);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o16[i] = f2_to_e4m3x2(o[2 * i] * inv, o[2 * i + 1] * inv);
+        if (valid) {
+          *reinterpret_cast<uint2*>(q + (int64_t)row * hidden + u * 8) = packed;
+          if ((u & 3) == 0) sf[sf_off(row, (u * 8) >> 5, kb_total)] = uint8_t(e + 127);
+        }
+      }
+    }
+  }
+  // completion: the last CTA resets this parity's counters and advances the epoch
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t t = atomicAdd(ticket, 1u);
+    if (t == gridDim.x - 1) {
+      uint32_t* cnt = counters(mine, p);
+      for (int src = 0; src < peers.world; ++src) atomicExch(cnt + src, 0u);
+      *ticket = 0u;
+      __threadfence();
+      atomicAdd(epoch, 1u);
+    }
+  }
+}
+
+}  // namespace comm
+}  // namespace b200
+
+int b200_ar_push(const void* x, int T, int hidden, const ArPeers* peers, const uint32_t* epoch, int nctas,
+                 cudaStream_t st) {
+  if (T <= 0) return 0;
+  if (T > peers->max_t || hidden % 8 || peers->world > kArMaxRanks || nctas <= 0) return -1;
+  b200::comm::ar_push_kernel<<<nctas, b200::comm::kThreads, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(x), T,
+                                                                      hidden, *peers, epoch);
+  return cudaGetLastError() == cudaSuccess ? 0 : 1;
+}
+
+int b200_ar_reduce_norm(int T, int hidden, const ArPeers* peers, uint32_t* epoch, uint32_t* ticket, int push_ctas,
+                        float* residual, const float* w, float eps, void* y, uint8_t* q, uint8_t* sf, uint32_t* err,
+                        cudaStream_t st) {
+  if (T <= 0) return 0;
+  if (T > peers->max_t || hidden % 32 || hidden > b200::comm::kThreads * 8 * b200::comm::kMaxIt) return -1;
+  b200::comm::ar_reduce_norm_kernel<<<T, b200::comm::kThreads, 0, st>>>(
+      T, hidden, *peers, epoch, ticket, (uint32_t)push_ctas, residual, w, eps,
+      reinterpret_cast<__nv_bfloat16*>(y), q, sf, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : 1;
+}

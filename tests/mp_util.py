@@ -18,7 +18,7 @@ def free_port() -> int:
 
 def _worker(rank, world, port, fn, args, outdir):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
-                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     try:
         res = fn(rank, world, *args)
         torch.save({"ok": True, "res": res}, os.path.join(outdir, f"r{rank}.pt"))

@@ -1,0 +1,49 @@
+"""OpenAI-compatible server on the CPU engine (tiny model)."""
+import json
+
+import pytest
+
+
+@pytest.fixture(scope="module")
+def client():
+    from fastapi.testclient import TestClient
+    from b200ds import EngineConfig, load_engine
+    from b200ds.engine.tokenizer import ByteTokenizer
+    from b200ds.server.openai import EngineWorker, create_app
+    eng = load_engine("tiny", ecfg=EngineConfig(page_size=8, cuda_graphs=False), device="cpu")
+    tok = ByteTokenizer()
+    eng.tokenizer = tok
+    worker = EngineWorker(eng, tok).start()
+    with TestClient(create_app(worker, "tiny")) as c:
+        yield c
+    worker.stop()
+
+
+def test_completion_greedy_matches_engine(client):
+    r = client.post("/v1/completions", json={"prompt": [5, 6, 7, 8], "max_tokens": 6, "temperature": 0})
+    assert r.status_code == 200
+    body = r.json()
+    ids = body["choices"][0]["token_ids"]
+    assert len(ids) == 6 and body["usage"]["completion_tokens"] == 6
+    # greedy is deterministic: the same request gives the same tokens
+    r2 = client.post("/v1/completions", json={"prompt": [5, 6, 7, 8], "max_tokens": 6, "temperature": 0})
+    assert r2.json()["choices"][0]["token_ids"] == ids
+
+
+def test_completion_stream(client):
+    with client.stream("POST", "/v1/completions",
+                       json={"prompt": "hello", "max_tokens": 5, "temperature": 0, "stream": True}) as r:
+        events = [l for l in r.iter_lines() if l.startswith("data: ")]
+    assert events[-1] == "data: [DONE]"
+    toks = sum((json.loads(e[6:])["choices"][0].get("token_ids") or [] for e in events[:-1]), [])
+    assert len(toks) == 5
+
+
+def test_chat_and_models_and_metrics(client):
+    r = client.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "hi"}],
+                                                  "max_tokens": 4, "temperature": 0.8, "seed": 3})
+    assert r.status_code == 200
+    assert r.json()["choices"][0]["message"]["role"] == "assistant"
+    assert client.get("/v1/models").json()["data"][0]["id"] == "tiny"
+    m = client.get("/metrics").text
+    assert "b200ds_requests_completed_total" in m
