@@ -46,10 +46,13 @@ class Linear:
 
     @property
     def out_features(self) -> int:
-        return self.w.shape[0]
+        rows = getattr(self.w, "rows", None)
+        return rows if rows is not None else self.w.shape[0]
 
     def __call__(self, x, out_dtype=torch.bfloat16) -> torch.Tensor:
-        return ops.linear(x, self.w, out_dtype)
+        y = ops.linear(x, self.w, out_dtype)
+        n = self.out_features
+        return y if y.shape[-1] == n else y[..., :n]
 
 
 @dataclass
@@ -158,6 +161,9 @@ class DeepseekModel:
         o_lat = ops.mla_attention(q_abs, q_pe, self.kv_cache[i], self.kv_scale[i], fb,
                                   c.softmax_scale, self.page_size, topk)
         o = ops.absorb_o(o_lat, aw.w_uv)                                  # [T, Hl*v]
+        if self.device.type == "cuda" and self.ps.tp_size > 1:
+            # leave the o_proj GEMM to the all-reduce so it can run fused
+            return ops.PendingLinear(o, aw.o_proj.w, aw.o_proj.out_features)
         return aw.o_proj(o, out_dtype=torch.float32 if self.device.type == "cpu" else torch.bfloat16)
 
     def _indexer(self, i, aw: AttnWeights, h, q_lat, fb: ForwardBatch):
@@ -177,11 +183,20 @@ class DeepseekModel:
     def _ffn(self, i: int, lw: LayerWeights, h, fb: ForwardBatch) -> torch.Tensor:
         c = self.cfg
         out_dt = torch.float32 if self.device.type == "cpu" else torch.bfloat16
+        fuse = self.device.type == "cuda" and self.ps.tp_size > 1
         if isinstance(lw.ffn, DenseWeights):
             a = ops.gate_up_swiglu(h, lw.ffn.gate_up)
+            if fuse:
+                return ops.PendingLinear(a, lw.ffn.down.w, lw.ffn.down.out_features)
             return lw.ffn.down(a, out_dtype=out_dt)
         mw: MoEWeights = lw.ffn
         w, ids = ops.router(h, mw.gate, mw.bias, c)
+        if fuse and ops.get_impl() == "native":
+            part = ops.moe_experts(h, w, ids, mw.experts, out_dtype=out_dt, n_experts_total=c.n_routed_experts,
+                                   combine=False)
+            if mw.shared_gate_up is not None:
+                part.add = lw.ffn.shared_down(ops.gate_up_swiglu(h, mw.shared_gate_up), out_dtype=out_dt)
+            return part
         out = ops.moe_experts(h, w, ids, mw.experts, out_dtype=out_dt, n_experts_total=c.n_routed_experts)
         if mw.shared_gate_up is not None:
             s = lw.ffn.shared_down(ops.gate_up_swiglu(h, mw.shared_gate_up), out_dtype=out_dt)

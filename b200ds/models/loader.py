@@ -27,15 +27,16 @@ def _quantize(w: torch.Tensor, fmt: str, device) -> object:
     if fmt in ("fp32", "bf16"):
         return w.to(device=device, dtype=torch.float32 if fmt == "fp32" else torch.bfloat16)
     if fmt == "mxfp8":
+        rows = w.shape[0]
         if w.shape[0] % 128:
             w = torch.cat([w, torch.zeros(128 - w.shape[0] % 128, w.shape[1], dtype=w.dtype)], 0)
         wd = w.to(device)
         if wd.is_cuda:
             from .. import ops
             a = ops.quant(wd.to(torch.bfloat16))
-            return MXFP8Tensor(a.q, a.sf)
+            return MXFP8Tensor(a.q, a.sf, rows)
         q, sf = quant_mxfp8_ref(wd.float())
-        return MXFP8Tensor(q, sf)
+        return MXFP8Tensor(q, sf, rows)
     raise ValueError(f"unknown weight format {fmt}")
 
 

@@ -50,7 +50,7 @@ def rand_mx(shape_lead, N: int, K: int, dev, seeder: _Seeder) -> MXFP8Tensor:
     if Np != N:
         data[..., N:, :] = 0
     sf = torch.full((*shape_lead, Np * K // 32), SCALE_BYTE, dtype=torch.uint8, device=dev)
-    return MXFP8Tensor(data.view(torch.float8_e4m3fn), sf)
+    return MXFP8Tensor(data.view(torch.float8_e4m3fn), sf, N)
 
 
 def rand_bf16(shape, dev, gen, std=0.02, dtype=torch.bfloat16):

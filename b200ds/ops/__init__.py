@@ -69,6 +69,39 @@ class ExpertWeights:
     inter: int
 
 
+@dataclass
+class PendingLinear:
+    """y = x W^T left uncomputed so the following all-reduce can run inside
+    the GEMM's epilogue (fused GEMM + all-reduce)."""
+    x: object
+    w: object
+    n_out: int
+
+
+@dataclass
+class MoEPartial:
+    """Rank-partial MoE output before the combine: weighted expert rows
+    y[rows, h], their per-(token, k) row index pair_row[T, K] (-1 = expert on
+    another rank), and an optional additive partial (shared expert)."""
+    y: torch.Tensor
+    pair_row: torch.Tensor
+    add: Optional[torch.Tensor] = None
+
+
+def materialize(a, out_dtype=torch.bfloat16) -> torch.Tensor:
+    if isinstance(a, PendingLinear):
+        y = linear(a.x, a.w, out_dtype)
+        return y if y.shape[-1] == a.n_out else y[..., : a.n_out]
+    if isinstance(a, MoEPartial):
+        from . import cuda
+        T = a.pair_row.shape[0]
+        out = torch.empty(T, a.y.shape[1], dtype=out_dtype, device=a.y.device)
+        add = a.add.to(torch.bfloat16).contiguous() if a.add is not None else None
+        cuda._C.moe_combine(a.y, a.pair_row, add, out)
+        return out
+    return a
+
+
 def to_float(x) -> torch.Tensor:
     if isinstance(x, QAct):
         if x.hf is not None:
@@ -116,9 +149,12 @@ def allreduce_add_rmsnorm(a: torch.Tensor, residual: torch.Tensor, w: torch.Tens
                           ps, kind: str, next_linear=None):
     """All-reduce the rank-partial output ``a`` over the TP group, add it to
     the residual stream, RMSNorm, and quantize for ``next_linear``.
-    Returns (normalized activation, new residual)."""
-    if a.is_cuda and ps.tp_size > 1 and _IMPL == "native":
+    Returns (normalized activation, new residual).  ``a`` may be a
+    PendingLinear / MoEPartial, which the fused path folds into its GEMM or
+    combine kernel."""
+    if residual.is_cuda and ps.tp_size > 1 and _IMPL == "native":
         return _native().allreduce_add_rmsnorm(a, residual, w, eps, ps, next_linear)
+    a = materialize(a, torch.float32 if not residual.is_cuda else torch.bfloat16)
     if ps.tp_size > 1 or (kind == "ffn" and ps.ep_size > 1):
         if ps.tp_size > 1:
             ps.tp_all_reduce(a)
@@ -244,12 +280,12 @@ def router(h, gate: torch.Tensor, bias: torch.Tensor, cfg):
 
 
 def moe_experts(h, w: torch.Tensor, ids: torch.Tensor, ex: ExpertWeights, out_dtype=torch.float32,
-                n_experts_total=None):
+                n_experts_total=None, combine: bool = True):
     """Local-expert part of the MoE: sum_k w[t,k] * expert_{ids[t,k]}(h[t]) over
     the experts this rank owns (others contribute on their ranks)."""
     if isinstance(ex.w13, MXFP8Tensor) and (h.q if isinstance(h, QAct) else h).is_cuda:
         if _IMPL == "native":
-            return _native().moe_experts(h, w, ids, ex, out_dtype, n_experts_total)
+            return _native().moe_experts(h, w, ids, ex, out_dtype, n_experts_total, combine)
         from . import baseline
         return baseline.moe_experts(h if isinstance(h, QAct) else quant(h), w, ids, ex, out_dtype)
     xf = to_float(h)

@@ -86,14 +86,20 @@ def allreduce_add_rmsnorm(a, residual, w, eps, ps, next_linear=None):
     """TP all-reduce + residual add + RMSNorm (+ MXFP8 quant): one fused
     NVLink kernel pair when the symmetric workspace is set up and the step
     fits it, else NCCL followed by the fused add+norm kernel."""
+    from . import MoEPartial, PendingLinear, materialize
     far = getattr(ps, "fused_ar", None)
-    if far is not None and far.supports(a.shape[0]):
+    T = residual.shape[0]
+    if far is not None and far.supports(T):
         quantized = next_linear is not None and getattr(next_linear, "quantized", False)
         if residual.dtype != torch.float32:
             residual = residual.float()
-        return far.allreduce_add_rmsnorm(a, residual, w, eps, quantized)
+        if isinstance(a, PendingLinear) and isinstance(a.w, MXFP8Tensor) and a.n_out == a.w.data.shape[0]:
+            return far.gemm_allreduce_add_rmsnorm(a.x, a.w, residual, w, eps, quantized)
+        if isinstance(a, MoEPartial):
+            return far.moe_allreduce_add_rmsnorm(a, residual, w, eps, quantized)
+        return far.allreduce_add_rmsnorm(materialize(a), residual, w, eps, quantized)
     from . import comm
-    a = comm.all_reduce(a, ps)
+    a = comm.all_reduce(materialize(a), ps)
     return add_rmsnorm_act(a, residual, w, eps, next_linear)
 
 
@@ -211,7 +217,8 @@ def moe_tile_n(rows_per_expert: float, cap: int) -> int:
     return cap
 
 
-def moe_experts(h, w: torch.Tensor, ids: torch.Tensor, ex, out_dtype=torch.bfloat16, n_experts_total=None):
+def moe_experts(h, w: torch.Tensor, ids: torch.Tensor, ex, out_dtype=torch.bfloat16, n_experts_total=None,
+                combine: bool = True):
     """Local-expert MoE: routing layout -> row gather -> persistent FC1
     (SwiGLU + MXFP8 requant) -> persistent FC2 (routing-weighted) -> combine.
     No host synchronisation: buffers are sized for the worst case."""
@@ -247,6 +254,9 @@ def moe_experts(h, w: torch.Tensor, ids: torch.Tensor, ex, out_dtype=torch.bfloa
     y = torch.empty(max_rows, Hd, dtype=torch.bfloat16, device=dev)
     _C.gemm_grouped(w2.data, w2.sf, hq.q, hq.sf, Hd, I, E, 0, bn2, seg_start, seg_count, tt2, 3,
                     y, Hd, None, None, 0, row_weight, 0, True)
+    if not combine:
+        from . import MoEPartial
+        return MoEPartial(y, pair_row, None)
     out = torch.empty(T, Hd, dtype=out_dtype, device=dev)
     _C.moe_combine(y, pair_row, None, out)
     return out

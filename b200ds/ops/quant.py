@@ -85,9 +85,11 @@ def unpack_sf(packed: torch.Tensor, rows: int, k: int) -> torch.Tensor:
 
 @dataclass
 class MXFP8Tensor:
-    """Row-wise MXFP8 matrix: data [R, K] e4m3, scales in sf128x4 layout."""
+    """Row-wise MXFP8 matrix: data [R, K] e4m3, scales in sf128x4 layout.
+    ``rows`` is the logical row count when R was padded to a multiple of 128."""
     data: torch.Tensor
     sf: torch.Tensor
+    rows: Optional[int] = None
 
     @property
     def shape(self):

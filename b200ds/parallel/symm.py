@@ -64,6 +64,51 @@ class FusedAllReduce:
             return qa, residual
         return y, residual
 
+    def _outs(self, T, H, dev, quantize, keep_bf16=True):
+        from ..ops.cuda import alloc_qact
+        y = torch.empty(T, H, dtype=torch.bfloat16, device=dev) if (keep_bf16 or not quantize) else None
+        qa = alloc_qact(T, H, dev) if quantize else None
+        return y, qa
+
+    def _reduce(self, T, H, push_ctas, residual, w, eps, y, qa):
+        from .. import _C
+        _C.ar_reduce_norm(T, H, self.bases, self.rank, self.max_tokens, self.epoch, self.ticket, push_ctas,
+                          residual, w, eps, y, qa.q if qa else None, qa.sf if qa else None, self.err)
+        if qa is not None:
+            qa.hf = y
+            return qa, residual
+        return y, residual
+
+    def gemm_allreduce_add_rmsnorm(self, x, wq, residual, ln_w, eps, quantize):
+        """o_proj / down_proj GEMM whose split-K cluster epilogue pushes the
+        output tiles into every rank's slot, then reduce + residual + norm."""
+        from .. import _C
+        from ..ops import QAct
+        from ..ops.cuda import choose_splits, quant
+        a = x if isinstance(x, QAct) else quant(x)
+        T, K = a.q.shape
+        N = wq.data.shape[0]
+        splits = choose_splits(T, N, K)
+        if splits < 2 or T > 128:
+            from ..ops.cuda import gemm
+            return self.allreduce_add_rmsnorm(gemm(a, wq), residual, ln_w, eps, quantize)
+        n = _C.gemm_push(wq.data, wq.sf, a.q, a.sf, N, T, K, splits, self.bases, self.rank, self.max_tokens,
+                         self.epoch)
+        y, qa = self._outs(T, N, a.q.device, quantize)
+        return self._reduce(T, N, int(n), residual, ln_w, eps, y, qa)
+
+    def moe_allreduce_add_rmsnorm(self, part, residual, ln_w, eps, quantize):
+        """MoE combine (local experts + shared partial) pushed straight into
+        every rank's slot, then reduce + residual + norm."""
+        from .. import _C
+        T = part.pair_row.shape[0]
+        H = part.y.shape[1]
+        add = part.add.to(torch.bfloat16).contiguous() if part.add is not None else None
+        _C.moe_combine_push(part.y, part.pair_row, add, self.bases, self.rank, self.max_tokens, self.epoch,
+                            self.push_ctas)
+        y, qa = self._outs(T, H, part.y.device, quantize)
+        return self._reduce(T, H, self.push_ctas, residual, ln_w, eps, y, qa)
+
     def check(self) -> None:
         """Raise if a bounded wait inside the kernels timed out."""
         e = int(self.err.item())

@@ -243,13 +243,23 @@ def main():
                        "l2": "no flush: per-step weights+KV >> 126 MB L2", "init_s": round(t_init, 1)},
         }
         print(json.dumps(out), flush=True)
+    # Teardown: drop every reference to the captured graphs (they hold NCCL
+    # work) before the process group goes; a watchdog ends the process if the
+    # teardown stalls, since the result line is already out.
+    gr = None
     eng.graphs.release()
+    import gc
+    gc.collect()
     torch.cuda.synchronize()
     if world > 1:
+        threading.Timer(30.0, lambda: os._exit(0)).start()
         try:
             dist.destroy_process_group()
-        except Exception as e:  # the result line is already out
+        except Exception as e:
             log(f"process-group teardown: {e}")
+    sys.stdout.flush()
+    sys.stderr.flush()
+    os._exit(0)
 
 
 def count_launches(gr) -> int:

@@ -99,6 +99,41 @@ void gemm(const at::Tensor& w, const at::Tensor& w_sf, int64_t w_sf_estride, con
   check(b200_gemm_mxf8(&a, cur_stream()), "gemm_mxf8");
 }
 
+// Fused GEMM + all-reduce push: out tile rows go to every rank's receive slot.
+// Returns the number of CTAs that publish (the reduce kernel's expected count).
+int64_t gemm_push(const at::Tensor& w, const at::Tensor& w_sf, const at::Tensor& x, const at::Tensor& x_sf,
+                  int64_t nw, int64_t t, int64_t k, int64_t splits, std::vector<int64_t> bases, int64_t rank,
+                  int64_t max_t, const at::Tensor& epoch) {
+  check_cuda(w, "w");
+  const c10::cuda::CUDAGuard g(w.device());
+  TORCH_CHECK(k % 128 == 0 && nw % 128 == 0, "k, nw multiples of 128");
+  TORCH_CHECK(bases.size() >= 1 && bases.size() <= (size_t)kArMaxRanks, "1..8 ranks");
+  ArPeers pe{};
+  for (size_t i = 0; i < bases.size(); ++i) pe.base[i] = reinterpret_cast<uint8_t*>(bases[i]);
+  pe.rank = rank;
+  pe.world = bases.size();
+  pe.max_t = max_t;
+  GemmArgs a{};
+  a.w = ptr<uint8_t>(w);
+  a.w_sf = ptr<uint8_t>(w_sf);
+  a.x = ptr<uint8_t>(x);
+  a.x_sf = ptr<uint8_t>(x_sf);
+  a.x_rows = x.size(0);
+  a.nw = nw;
+  a.nw_total = w.numel() / k;
+  a.t = t;
+  a.k = k;
+  a.splits = splits;
+  a.epi = kEpiClusterPush;
+  a.ldo = nw;
+  a.ar_peers = &pe;
+  a.ar_epoch = reinterpret_cast<const uint32_t*>(epoch.data_ptr());
+  a.pdl = 1;
+  check(b200_gemm_mxf8(&a, cur_stream()), "gemm_push");
+  const int64_t bn = t <= 16 ? 16 : t <= 32 ? 32 : t <= 64 ? 64 : 128;
+  return (nw / 128) * ((t + bn - 1) / bn) * splits;
+}
+
 void rope(at::Tensor x, const at::Tensor& pos, const at::Tensor& table) {
   check_cuda(x, "x");
   const c10::cuda::CUDAGuard g(x.device());
@@ -250,6 +285,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm", &rmsnorm);
   m.def("quant", &quant);
   m.def("gemm", &gemm);
+  m.def("gemm_push", &gemm_push);
   m.def("rope", &rope);
   m.def("kv_store", &kv_store);
   m.def("router", &router);

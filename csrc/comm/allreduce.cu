@@ -231,3 +231,76 @@ int b200_ar_reduce_norm(int T, int hidden, const ArPeers* peers, uint32_t* epoch
       reinterpret_cast<__nv_bfloat16*>(y), q, sf, err);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
+
+// ---------------------------------------------------------------------------
+// MoE combine fused with the all-reduce push: for token t, the rank-partial
+// sum over its local experts' weighted rows y[pair_row[t, j]] plus the
+// shared-expert partial add[t] goes straight into recv[p][rank][t] of every
+// rank.  grid: `nctas` CTAs over the tokens.
+namespace b200 {
+namespace comm {
+__global__ void __launch_bounds__(kThreads) moe_combine_push_kernel(const __nv_bfloat16* __restrict__ y,
+                                                                     const int* __restrict__ pair_row, int T, int K,
+                                                                     int hidden, const __nv_bfloat16* __restrict__ add,
+                                                                     ArPeers peers, const uint32_t* epoch) {
+  pdl_wait();
+  const int p = (*epoch) & 1;
+  const int vec_per_row = hidden / 8;
+  const int64_t nvec = (int64_t)T * vec_per_row;
+  const int64_t per = (nvec + gridDim.x - 1) / gridDim.x;
+  const int64_t v0 = blockIdx.x * per, v1 = min(nvec, v0 + per);
+  for (int64_t v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
+    const int t = int(v / vec_per_row);
+    const int c = int(v - (int64_t)t * vec_per_row) * 8;
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    for (int j = 0; j < K; ++j) {
+      const int r = __ldcg(pair_row + t * K + j);
+      if (r < 0) continue;
+      const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(y + (int64_t)r * hidden + c));
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h[i]);
+        acc[2 * i] += f.x;
+        acc[2 * i + 1] += f.y;
+      }
+    }
+    if (add) {
+      const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(add + (int64_t)t * hidden + c));
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h[i]);
+        acc[2 * i] += f.x;
+        acc[2 * i + 1] += f.y;
+      }
+    }
+    uint4 outv;
+    __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&outv);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+    for (int q = 0; q < peers.world; ++q) {
+      __nv_bfloat16* dst = recv_slot(peers.base[q], p, peers.rank, peers.world, peers.max_t, hidden);
+      *reinterpret_cast<uint4*>(dst + (int64_t)t * hidden + c) = outv;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int q = 0; q < peers.world; ++q) red_release_sys_add(counters(peers.base[q], p) + peers.rank, 1u);
+  }
+}
+}  // namespace comm
+}  // namespace b200
+
+int b200_moe_combine_push(const void* y, const int* pair_row, int T, int K, int hidden, const void* add,
+                          const ArPeers* peers, const uint32_t* epoch, int nctas, cudaStream_t st) {
+  if (T <= 0) return 0;
+  if (T > peers->max_t || hidden % 8 || nctas <= 0) return -1;
+  b200::comm::moe_combine_push_kernel<<<nctas, b200::comm::kThreads, 0, st>>>(
+      reinterpret_cast<const __nv_bfloat16*>(y), pair_row, T, K, hidden, reinterpret_cast<const __nv_bfloat16*>(add),
+      *peers, epoch);
+  return cudaGetLastError() == cudaSuccess ? 0 : 1;
+}

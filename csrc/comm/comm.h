@@ -23,3 +23,5 @@ int b200_ar_push(const void* x, int T, int hidden, const ArPeers* peers, const u
 int b200_ar_reduce_norm(int T, int hidden, const ArPeers* peers, uint32_t* epoch, uint32_t* ticket, int push_ctas,
                         float* residual, const float* w, float eps, void* y, uint8_t* q, uint8_t* sf, uint32_t* err,
                         cudaStream_t st);
+int b200_moe_combine_push(const void* y, const int* pair_row, int T, int K, int hidden, const void* add,
+                          const ArPeers* peers, const uint32_t* epoch, int nctas, cudaStream_t st);

@@ -48,6 +48,20 @@ void ar_reduce_norm(int64_t T, int64_t hidden, std::vector<int64_t> bases, int64
   TORCH_CHECK(rc == 0, "ar_reduce_norm failed ", rc);
 }
 
+void moe_combine_push(const at::Tensor& y, const at::Tensor& pair_row, c10::optional<at::Tensor> add,
+                      std::vector<int64_t> bases, int64_t rank, int64_t max_t, const at::Tensor& epoch, int64_t nctas) {
+  TORCH_CHECK(y.is_cuda() && y.scalar_type() == at::kBFloat16 && y.is_contiguous(), "y bf16");
+  TORCH_CHECK(pair_row.scalar_type() == at::kInt && pair_row.is_contiguous(), "pair_row int32 [T,K]");
+  if (add.has_value()) TORCH_CHECK(add->scalar_type() == at::kBFloat16 && add->is_contiguous(), "add bf16 [T,H]");
+  const c10::cuda::CUDAGuard g(y.device());
+  ArPeers p = make_peers(bases, rank, max_t);
+  const int rc = b200_moe_combine_push(y.data_ptr(), reinterpret_cast<const int*>(pair_row.data_ptr()), pair_row.size(0),
+                                       pair_row.size(1), y.size(1), optr<void>(add), &p,
+                                       reinterpret_cast<const uint32_t*>(epoch.data_ptr()), nctas,
+                                       at::cuda::getCurrentCUDAStream().stream());
+  TORCH_CHECK(rc == 0, "moe_combine_push failed ", rc);
+}
+
 int64_t ar_buffer_size(int64_t world, int64_t max_t, int64_t hidden) { return ar_buffer_bytes(world, max_t, hidden); }
 
 }  // namespace
@@ -56,4 +70,5 @@ void register_comm(pybind11::module& m) {
   m.def("ar_push", &ar_push);
   m.def("ar_reduce_norm", &ar_reduce_norm);
   m.def("ar_buffer_size", &ar_buffer_size);
+  m.def("moe_combine_push", &moe_combine_push);
 }

@@ -26,6 +26,7 @@
 // routed experts use trtllm-gen kernels (mo.py:19-40).
 #include "../common/ptx.cuh"
 #include "gemm_mxf8.h"
+#include "../comm/comm.h"
 
 namespace b200 {
 namespace gemm {
@@ -76,6 +77,8 @@ struct Params {
   // weighted store (MoE down): per sorted row weight
   const float* row_weight;
   uint32_t* err;
+  ArPeers peers;             // kEpiClusterPush
+  const uint32_t* ar_epoch;
 };
 
 // Byte offset of the scale byte for (row, kblock) inside a packed sf128x4
@@ -248,7 +251,7 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
     if (ok) {
       const uint32_t lane_addr = tmem_acc + (uint32_t(sub * 32) << 16);
       const int tmax = rows - tile_t * BN;           // valid token columns in this tile
-      if (EPI == kEpiClusterSplit) {
+      if (EPI == kEpiClusterSplit || EPI == kEpiClusterPush) {
         // stage this split's partial tile: red[row][BN+1] over the (drained) A stages
         float* red = reinterpret_cast<float*>(sA);
         const int row = sub * 32 + lane;
@@ -317,9 +320,13 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
 
   tc_fence_before();
   __syncthreads();
-  if constexpr (EPI == kEpiClusterSplit) {
+  if constexpr (EPI == kEpiClusterSplit || EPI == kEpiClusterPush) {
     // Every split of this output tile has staged its partial; CTA `rank`
     // sums rows [rank*RPC, (rank+1)*RPC) of the tile across the cluster.
+    // kEpiClusterPush stores the sums into recv[parity][my rank] of every
+    // rank (P2P over NVLink) and then publishes with one counter increment
+    // per rank, so the all-reduce transfer overlaps the remaining tiles.
+    const int parity = (EPI == kEpiClusterPush) ? int(__ldcg(p.ar_epoch) & 1u) : 0;
     cluster_sync();
     const int S = gridDim.z;
     const uint32_t rank = cluster_ctarank();
@@ -333,8 +340,27 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
         const uint32_t off = (uint32_t)(rr * (BN + 1) + col) * 4u;
         float acc = 0.f;
         for (int q = 0; q < S; ++q) acc += ld_dsmem_f32(mapa_shared(red_local + off, q));
-        reinterpret_cast<__nv_bfloat16*>(p.out)[(int64_t)(b_row + col) * p.ldo + tile_n * kTileM + rr] =
-            __float2bfloat16(acc);
+        const __nv_bfloat16 v = __float2bfloat16(acc);
+        const int64_t oi = (int64_t)(b_row + col) * p.ldo + tile_n * kTileM + rr;
+        if constexpr (EPI == kEpiClusterPush) {
+          for (int dst = 0; dst < p.peers.world; ++dst) {
+            __nv_bfloat16* slot = reinterpret_cast<__nv_bfloat16*>(p.peers.base[dst] + kArRecvOff) +
+                                  ((int64_t)(parity * p.peers.world + p.peers.rank) * p.peers.max_t) * p.ldo;
+            slot[oi] = v;
+          }
+        } else {
+          reinterpret_cast<__nv_bfloat16*>(p.out)[oi] = v;
+        }
+      }
+    }
+    if constexpr (EPI == kEpiClusterPush) {
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        __threadfence_system();
+        for (int dst = 0; dst < p.peers.world; ++dst) {
+          uint32_t* cnt = reinterpret_cast<uint32_t*>(p.peers.base[dst]) + parity * kArMaxRanks + p.peers.rank;
+          asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(cnt), "r"(1u) : "memory");
+        }
       }
     }
     cluster_sync();
@@ -405,6 +431,10 @@ static int launch_t(const GemmArgs& a, cudaStream_t st) {
   p.inter = a.inter;
   p.row_weight = a.row_weight;
   p.err = a.err;
+  if (EPI == kEpiClusterPush) {
+    p.peers = *reinterpret_cast<const ArPeers*>(a.ar_peers);
+    p.ar_epoch = a.ar_epoch;
+  }
   auto kern = gemm_mxf8_kernel<BN, EPI, GROUPED>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   dim3 grid;
@@ -421,7 +451,7 @@ static int launch_t(const GemmArgs& a, cudaStream_t st) {
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = a.pdl ? 1 : 0;
   int nattr = 1;
-  if (EPI == kEpiClusterSplit) {
+  if (EPI == kEpiClusterSplit || EPI == kEpiClusterPush) {
     attr[1].id = cudaLaunchAttributeClusterDimension;
     attr[1].val.clusterDim.x = 1;
     attr[1].val.clusterDim.y = 1;
@@ -462,6 +492,9 @@ int b200_gemm_mxf8(const GemmArgs* a, cudaStream_t st) {
     case kEpiClusterSplit:
       if (g || a->splits < 2 || a->splits > 8 || (128 % a->splits) != 0 || a->t > 128) return -13;
       return launch_bn<kEpiClusterSplit, false>(*a, st);
+    case kEpiClusterPush:
+      if (g || a->splits < 2 || a->splits > 8 || (128 % a->splits) != 0 || a->t > 128 || !a->ar_peers) return -14;
+      return launch_bn<kEpiClusterPush, false>(*a, st);
   }
   return -12;
 }

@@ -9,6 +9,8 @@ enum GemmEpi : int {
   kEpiSwiglu = 2,        // q_out/sf_out = mxfp8(silu(gate) * up)
   kEpiWeightedBf16 = 3,  // out[row, n] = bf16(acc * row_weight[row])  (grouped only)
   kEpiClusterSplit = 4,  // split-K over a thread-block cluster, DSMEM reduction, bf16 out
+  kEpiClusterPush = 5,   // as kEpiClusterSplit, but the reduced tile is pushed into every
+                         // rank's all-reduce receive slot (fused GEMM + all-reduce)
 };
 
 struct GemmArgs {
@@ -37,6 +39,9 @@ struct GemmArgs {
   const float* row_weight;
   uint32_t* err;
   int pdl;
+  // kEpiClusterPush: symmetric all-reduce buffers (see comm/comm.h)
+  const void* ar_peers;     // const ArPeers*
+  const uint32_t* ar_epoch;
 };
 
 int b200_gemm_mxf8(const GemmArgs* args, cudaStream_t stream);

