@@ -197,9 +197,17 @@ def mla_attention(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size, to
 
 
 # ---------------------------------------------------------------------------
+_GATE_BF16 = {}
+
+
 def router(x: torch.Tensor, gate: torch.Tensor, bias: torch.Tensor, cfg):
-    logits = torch.matmul(x.float(), gate.float().t()) if gate.dtype == torch.float32 else \
-        torch.matmul(x.to(gate.dtype), gate.t()).float()
+    """Router logits on the tensor cores (bf16 inputs, fp32 accumulate and
+    output), then the fused sigmoid / group-limited top-k kernel."""
+    g16 = _GATE_BF16.get(gate.data_ptr())
+    if g16 is None or g16.shape != gate.shape:
+        g16 = gate.to(torch.bfloat16).contiguous()
+        _GATE_BF16[gate.data_ptr()] = g16
+    logits = torch.mm(x.to(torch.bfloat16), g16.t(), out_dtype=torch.float32)
     T = logits.shape[0]
     K = cfg.num_experts_per_tok
     w = torch.empty(T, K, dtype=torch.float32, device=x.device)

@@ -19,7 +19,7 @@ import torch.distributed as dist
 
 
 class FusedAllReduce:
-    def __init__(self, ps, hidden: int, max_tokens: int = 256, push_ctas: int = 32):
+    def __init__(self, ps, hidden: int, max_tokens: int = 256, push_ctas: int = 296):
         import torch.distributed._symmetric_memory as symm_mem
         from .. import _C
         self.ps = ps

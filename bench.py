@@ -214,6 +214,8 @@ def main():
     h2d = args.batch * (4 + 4 + 8 + 4) + args.batch * eng.graphs.max_pages * 4
     d2h = args.batch * 8
     launches = count_launches(gr) if args.impl == "native" else None
+    if os.environ.get("B200_BENCH_PROFILE") == "1":
+        profile_breakdown(gr, ps.rank)
     clocks = sampler.summary()
     if ps.rank == 0:
         out = {
@@ -260,6 +262,25 @@ def main():
     sys.stdout.flush()
     sys.stderr.flush()
     os._exit(0)
+
+
+def profile_breakdown(gr, rank: int) -> None:
+    """Diagnostic only (stderr, never part of the result): per-kernel device
+    time of one untimed decode-graph replay."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        gr.graph.replay()
+        torch.cuda.synchronize()
+    if rank != 0:
+        return
+    rows = sorted(prof.key_averages(), key=lambda e: -e.device_time_total)
+    tot = sum(e.device_time_total for e in rows)
+    print(f"[profile] kernel time {tot / 1e3:.2f} ms in one replay", file=sys.stderr)
+    for e in rows[:28]:
+        print(f"[profile] {e.device_time_total / 1e3:8.3f} ms {100 * e.device_time_total / max(tot, 1):5.1f}% "
+              f"n={e.count:4d} {e.key[:100]}", file=sys.stderr)
 
 
 def count_launches(gr) -> int:
