@@ -138,13 +138,26 @@ def gemm(a, w: MXFP8Tensor, out_dtype=torch.bfloat16) -> torch.Tensor:
     return out
 
 
-def gemm_swiglu_quant(a, w: MXFP8Tensor):
+def swiglu_splits(T: int, I: int, K: int) -> int:
+    """Cluster split-K for thin gate_up GEMMs (few 128-channel tiles)."""
+    if T > 128:
+        return 1
+    tiles = I // 128
+    ktiles = K // 128
+    for s in (4, 2):
+        if tiles * s <= 148 and ktiles // s >= 4:
+            return s
+    return 1
+
+
+def gemm_swiglu_quant(a, w: MXFP8Tensor, splits: Optional[int] = None):
     """MXFP8 act [T, K] x gate_up [2I, K] -> MXFP8(silu(g) * u) [T, I]."""
     T, K = a.q.shape
     I = w.data.shape[0] // 2
     o = alloc_qact(T, I, a.q.device)
-    _C.gemm(w.data, w.sf, 0, a.q, a.sf, 2 * I, T, K, 2, 1, None, 0, o.q, o.sf, I, I, 0, None, None, 0, None, None,
-            False)
+    s = swiglu_splits(T, I, K) if splits is None else splits
+    _C.gemm(w.data, w.sf, 0, a.q, a.sf, 2 * I, T, K, 6 if s > 1 else 2, s, None, 0, o.q, o.sf, I, I, 0, None, None,
+            0, None, None, s > 1)
     return o
 
 

@@ -41,6 +41,7 @@ __global__ void __launch_bounds__(kThreads) mla_simt_kernel(const __nv_bfloat16*
   const int h0 = blockIdx.y * kHeads;
   const int nh = min(kHeads, H - h0);
   pdl_wait();
+  pdl_launch_dependents();   // dependents wait for this grid before touching its outputs
   const int b = q_seq[t];
   const int n = q_pos[t] + 1;
   const int nkeys = topk ? min(topk_n, n) : n;
@@ -152,7 +153,6 @@ __global__ void __launch_bounds__(kThreads) mla_simt_kernel(const __nv_bfloat16*
     for (int j = 0; j < L / 16; ++j)
       out[((int64_t)t * H + h0 + oh) * L + oc0 + 16 * j] = __float2bfloat16(acc[j] * inv);
   }
-  pdl_launch_dependents();
 }
 
 }  // namespace attn

@@ -113,6 +113,7 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
   const int split = blockIdx.z;
 
   pdl_wait();
+  pdl_launch_dependents();   // dependents wait for this grid before touching its outputs
   const int b = p.q_seq[t];
   const int n = p.q_pos[t] + 1;
   // KV tokens per split adapt to this query's own length (graph-safe).
@@ -362,7 +363,6 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
   }
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) pdl_launch_dependents();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, S::kTmemCols);
@@ -373,6 +373,7 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
 __global__ void mla_merge_kernel(const float* part_o, const float* part_lse, int nsplit, int TH, __nv_bfloat16* out) {
   const int th = blockIdx.x;
   pdl_wait();
+  pdl_launch_dependents();   // dependents wait for this grid before touching its outputs
   float M = -INFINITY;
   for (int s = 0; s < nsplit; ++s) M = fmaxf(M, part_lse[(int64_t)s * TH + th]);
   float w[16];
@@ -389,7 +390,6 @@ __global__ void mla_merge_kernel(const float* part_o, const float* part_lse, int
       if (w[s] != 0.f) acc += w[s] * part_o[((int64_t)s * TH + th) * kL + d];
     out[(int64_t)th * kL + d] = __float2bfloat16(acc * inv);
   }
-  pdl_launch_dependents();
 }
 
 // q_abs [T,H,512] bf16 + q_pe [T,H,64] bf16 -> e4m3 [T,H,576] with a per-(t,h) fp32 scale.
@@ -397,6 +397,7 @@ __global__ void q_quant_kernel(const __nv_bfloat16* q_abs, const __nv_bfloat16* 
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   pdl_wait();
+  pdl_launch_dependents();   // dependents wait for this grid before touching its outputs
   if (w >= TH) return;
   const __nv_bfloat16* a = q_abs + (int64_t)w * kL;
   const __nv_bfloat16* r = q_pe + (int64_t)w * kR;
@@ -418,7 +419,6 @@ __global__ void q_quant_kernel(const __nv_bfloat16* q_abs, const __nv_bfloat16* 
   dst[kL + lane] = uint8_t(f2_to_e4m3x2(v[16] * inv, 0.f) & 0xFF);
   dst[kL + lane + 32] = uint8_t(f2_to_e4m3x2(v[17] * inv, 0.f) & 0xFF);
   if (lane == 0) qs[w] = sc;
-  pdl_launch_dependents();
 }
 
 // ---------------------------------------------------------------------------

@@ -63,6 +63,7 @@ __device__ __forceinline__ __nv_bfloat16* recv_slot(uint8_t* base, int parity, i
 __global__ void __launch_bounds__(kThreads) ar_push_kernel(const __nv_bfloat16* __restrict__ x, int T, int hidden,
                                                            ArPeers peers, const uint32_t* epoch) {
   pdl_wait();
+  if (threadIdx.x == 0) pdl_launch_dependents();   // e.g. the next GEMM prefetches weights during our wait
   const int p = (*epoch) & 1;
   const int64_t n16 = (int64_t)T * hidden / 8;       // 16-byte vectors
   const int64_t per = (n16 + gridDim.x - 1) / gridDim.x;
@@ -87,6 +88,7 @@ __global__ void __launch_bounds__(kThreads) ar_reduce_norm_kernel(
   __shared__ float red[32];
   __shared__ int ok_s;
   pdl_wait();
+  if (threadIdx.x == 0) pdl_launch_dependents();   // e.g. the next GEMM prefetches weights during our wait
   const int p = (*epoch) & 1;
   uint8_t* mine = peers.base[peers.rank];
   if (threadIdx.x == 0) {
@@ -244,6 +246,7 @@ __global__ void __launch_bounds__(kThreads) moe_combine_push_kernel(const __nv_b
                                                                      int hidden, const __nv_bfloat16* __restrict__ add,
                                                                      ArPeers peers, const uint32_t* epoch) {
   pdl_wait();
+  if (threadIdx.x == 0) pdl_launch_dependents();   // e.g. the next GEMM prefetches weights during our wait
   const int p = (*epoch) & 1;
   const int vec_per_row = hidden / 8;
   const int64_t nvec = (int64_t)T * vec_per_row;

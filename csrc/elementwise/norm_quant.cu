@@ -107,6 +107,7 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const TX* __restrict_
   __shared__ float red[32];
   const int row = blockIdx.x;
   pdl_wait();
+  pdl_launch_dependents();   // dependents wait for this grid before touching its outputs
   const int units = K >> 3;
   float v[kMaxIt][8];
   float ss = 0.f;
@@ -149,7 +150,6 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const TX* __restrict_
     }
     if (q) quant8(o, q + (int64_t)row * K + u * 8, sf, row, u * 8, kb_total, u < units);
   }
-  pdl_launch_dependents();
 }
 
 // Plain MXFP8 quantization of x [rows, K] (bf16 or fp32).
@@ -160,10 +160,10 @@ __global__ void __launch_bounds__(kThreads) quant_kernel(const TX* __restrict__ 
   const int u = blockIdx.x * kThreads + threadIdx.x;
   const int units = K >> 3;
   pdl_wait();
+  pdl_launch_dependents();   // dependents wait for this grid before touching its outputs
   float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   if (u < units) load8<TX>(x + (int64_t)row * ldx + u * 8, v);
   quant8(v, q + (int64_t)row * K + u * 8, sf, row, u * 8, K >> 5, u < units);
-  pdl_launch_dependents();
 }
 
 }  // namespace ew

@@ -21,6 +21,7 @@ __global__ void rope_kernel(void* x, int f32, int64_t st_t, int64_t st_h, int H,
   const int t = blockIdx.x;
   const int half = d >> 1;
   pdl_wait();
+  pdl_launch_dependents();   // dependents wait for this grid before touching its outputs
   const int p = pos[t];
   for (int i = threadIdx.x; i < H * half; i += blockDim.x) {
     const int h = i / half, j = i % half;
@@ -38,7 +39,6 @@ __global__ void rope_kernel(void* x, int f32, int64_t st_t, int64_t st_h, int H,
       xp[base + 1] = __float2bfloat16(a * s + b * c);
     }
   }
-  pdl_launch_dependents();
 }
 
 // One warp per token: latent = rmsnorm(kv[:L]) * w, pe = rope(kv[L:L+R]);
@@ -49,6 +49,7 @@ __global__ void kv_store_kernel(const void* kv, int f32, int64_t ld, int T, int 
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   pdl_wait();
+  pdl_launch_dependents();   // dependents wait for this grid before touching its outputs
   if (warp >= T) return;
   const int64_t row = (int64_t)warp * ld;
   float ss = 0.f;
@@ -73,7 +74,6 @@ __global__ void kv_store_kernel(const void* kv, int f32, int64_t ld, int T, int 
     *reinterpret_cast<uint16_t*>(dst + L + 2 * j) = f2_to_e4m3x2((a * c - b * s) * inv_scale,
                                                                   (a * s + b * c) * inv_scale);
   }
-  pdl_launch_dependents();
 }
 
 // Router: one warp per token over E <= 256 experts (E % 32 == 0).
@@ -88,6 +88,7 @@ __global__ void router_kernel(const float* logits, const float* bias, int T, int
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   pdl_wait();
+  pdl_launch_dependents();   // dependents wait for this grid before touching its outputs
   if (warp >= T) return;
   const int per = E / 32;     // experts per lane, contiguous: lane owns [lane*per, lane*per+per)
   float sc[kMaxEPerLane], ch[kMaxEPerLane];
@@ -168,7 +169,6 @@ __global__ void router_kernel(const float* logits, const float* bias, int T, int
     w_out[(int64_t)warp * K + lane] = wk * norm * scaling;
     id_out[(int64_t)warp * K + lane] = idk;
   }
-  pdl_launch_dependents();
 }
 
 // ---------------------------------------------------------------------------
@@ -187,6 +187,7 @@ __global__ void moe_align_kernel(const int* ids, const float* w, int T, int K, i
   int* start = sh + E;    // [E]
   int* fill = sh + 2 * E; // [E]
   pdl_wait();
+  pdl_launch_dependents();   // dependents wait for this grid before touching its outputs
   for (int e = threadIdx.x; e < E; e += blockDim.x) { cnt[e] = 0; fill[e] = 0; }
   __syncthreads();
   const int n = T * K;
@@ -225,7 +226,6 @@ __global__ void moe_align_kernel(const int* ids, const float* w, int T, int K, i
       pair_row[i] = -1;
     }
   }
-  pdl_launch_dependents();
 }
 
 // Gather MXFP8 rows for the local experts: for routed pair i = (t, j) with a
@@ -235,6 +235,7 @@ __global__ void moe_gather_kernel(const uint8_t* xq, const uint8_t* xsf, const i
                                   int Kd, uint8_t* dq, uint8_t* dsf) {
   const int i = blockIdx.x;
   pdl_wait();
+  pdl_launch_dependents();   // dependents wait for this grid before touching its outputs
   if (i >= npairs) return;
   const int r = pair_row[i];
   if (r < 0) return;
@@ -248,7 +249,6 @@ __global__ void moe_gather_kernel(const uint8_t* xq, const uint8_t* xsf, const i
     const int64_t doff = ((int64_t)((r >> 7) * (kb >> 2) + (b >> 2)) << 9) + ((r & 31) << 4) + (((r & 127) >> 5) << 2) + (b & 3);
     dsf[doff] = xsf[so];
   }
-  pdl_launch_dependents();
 }
 
 // out[t, :] = sum_j y[pair_row[t*K+j], :] (+ add[t, :]) in fp32 -> bf16 / f32.
@@ -256,6 +256,7 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* y, const int* pair_row, 
                                    int add_f32, void* out, int out_f32) {
   const int t = blockIdx.x;
   pdl_wait();
+  pdl_launch_dependents();   // dependents wait for this grid before touching its outputs
   for (int c = threadIdx.x * 2; c < D; c += blockDim.x * 2) {
     float a0 = 0.f, a1 = 0.f;
     for (int j = 0; j < K; ++j) {
@@ -278,7 +279,6 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* y, const int* pair_row, 
           __floats2bfloat162_rn(a0, a1);
     }
   }
-  pdl_launch_dependents();
 }
 
 }  // namespace ew2

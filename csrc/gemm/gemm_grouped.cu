@@ -134,6 +134,7 @@ grouped_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
   const uint32_t tmem_sf = tmem + 2 * C::kAcc;
 
   pdl_wait();
+  if (threadIdx.x == 0) pdl_launch_dependents();   // dependents wait for this grid's completion
   const int total = __ldcg(p.ttile_off + p.E) * p.n_tiles;
   const int nk = p.k / kTileK;
   const int kc_total = p.k / kTileK;           // 512-byte sf chunks per 128 rows
@@ -287,7 +288,6 @@ grouped_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
   }
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) pdl_launch_dependents();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, C::kTmemCols);

@@ -38,12 +38,17 @@ constexpr int kSfChunk = 512;
 
 template <int BN, int EPI>
 struct Cfg {
-  static constexpr int kA = (EPI == kEpiSwiglu) ? 2 : 1;         // A tiles per stage
+  static constexpr bool kGateUp = (EPI == kEpiSwiglu || EPI == kEpiClusterSwiglu);
+  static constexpr int kA = kGateUp ? 2 : 1;                     // A tiles per stage
   static constexpr int kBChunks = (BN + 127) / 128;               // SF chunks for B
   static constexpr int kLoadBytes = kA * kTileM * kTileK + BN * kTileK + kA * kSfChunk + kBChunks * kSfChunk;
   static constexpr int kStageBytes = kLoadBytes + kSfChunk;   // + a repack chunk for the activation scales
   static constexpr int kStages0 = (200 * 1024) / kStageBytes;
-  static constexpr int kStages = kStages0 > 12 ? 12 : kStages0;
+  // Split-K cluster kernels stream few k-tiles per CTA: 4 stages keep two
+  // CTAs resident per SM (and twice as many clusters) instead of one.
+  static constexpr bool kCluster = (EPI == kEpiClusterSplit || EPI == kEpiClusterPush || EPI == kEpiClusterSwiglu);
+  static constexpr int kStagesCap = kCluster ? (kGateUp ? 3 : 4) : 12;
+  static constexpr int kStages = kStages0 > kStagesCap ? kStagesCap : kStages0;
   static constexpr int kAccCols = kA * BN;
   static constexpr int kSfColsA = 4 * kA;
   static constexpr int kSfColsB = 4 * kBChunks;
@@ -110,8 +115,11 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
   const int e = GROUPED ? blockIdx.z : 0;
   const int split = GROUPED ? 0 : blockIdx.z;
 
-  // Everything below may read what the previous kernel in the stream wrote.
-  pdl_wait();
+  // Programmatic dependent launch: let the next kernel start its prologue
+  // now (it waits for this grid's completion before touching our outputs).
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  // Grouped mode reads the routing layout the previous kernel wrote.
+  if (GROUPED) pdl_wait();
   int row0, rows;
   if (GROUPED) {
     row0 = p.seg_start[e];
@@ -161,30 +169,43 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
     // ------------------------------ producer ------------------------------
     if (lane == 0) {
       constexpr uint32_t bytes = C::kLoadBytes;
-      for (int i = 0; i < nk; ++i) {
+      const uint8_t* sfa_e = p.sfa + (GROUPED ? (int64_t)e * p.sfa_estride : 0);
+      const int kc_total = kb_total / 4;
+      // Weights never depend on the previous kernel: the first stages' weight
+      // tiles are in flight before griddepcontrol.wait, activations after it.
+      auto load_a = [&](int i) {
         const int s = i % C::kStages;
-        if (i >= C::kStages) {
-          if (!mbar_wait(&empty[s], ((i / C::kStages) - 1) & 1, p.err)) break;
-        }
         const int kt = kt0 + i;
         mbar_arrive_expect_tx(&full[s], bytes);
         uint8_t* a_dst = sA + (size_t)s * C::kA * kTileM * kTileK;
         tma_load_2d(a_dst, &tm_a, &full[s], kt * kTileK, a_row);
-        if (EPI == kEpiSwiglu) tma_load_2d(a_dst + kTileM * kTileK, &tm_a, &full[s], kt * kTileK, a_row + p.inter);
-        tma_load_2d(sB + (size_t)s * BN * kTileK, &tm_b, &full[s], kt * kTileK, b_row);
-        const uint8_t* sfa_e = p.sfa + (GROUPED ? (int64_t)e * p.sfa_estride : 0);
-        const int kc_total = kb_total / 4;
+        if (C::kGateUp) tma_load_2d(a_dst + kTileM * kTileK, &tm_a, &full[s], kt * kTileK, a_row + p.inter);
         uint8_t* sfa_dst = sSFA + (size_t)s * C::kA * kSfChunk;
         bulk_load(sfa_dst, sfa_e + ((int64_t)(tile_n * kc_total + kt) << 9), kSfChunk, &full[s]);
-        if (EPI == kEpiSwiglu) {
+        if (C::kGateUp) {
           const int rb_up = (p.inter + tile_n * kTileM) >> 7;
           bulk_load(sfa_dst + kSfChunk, sfa_e + ((int64_t)(rb_up * kc_total + kt) << 9), kSfChunk, &full[s]);
         }
+      };
+      auto load_b = [&](int i) {
+        const int s = i % C::kStages;
+        const int kt = kt0 + i;
+        tma_load_2d(sB + (size_t)s * BN * kTileK, &tm_b, &full[s], kt * kTileK, b_row);
         for (int c = 0; c < C::kBChunks; ++c) {
           const int rb = (b_row >> 7) + c;
           bulk_load(sSFB + ((size_t)s * C::kBChunks + c) * kSfChunk,
                     p.sfb + ((int64_t)(rb * kc_total + kt) << 9), kSfChunk, &full[s]);
         }
+      };
+      const int pre = nk < C::kStages ? nk : C::kStages;
+      for (int i = 0; i < pre; ++i) load_a(i);
+      if (!GROUPED) pdl_wait();
+      for (int i = 0; i < pre; ++i) load_b(i);
+      for (int i = pre; i < nk; ++i) {
+        const int s = i % C::kStages;
+        if (!mbar_wait(&empty[s], ((i / C::kStages) - 1) & 1, p.err)) break;
+        load_a(i);
+        load_b(i);
       }
     }
   } else if (warp == 1) {
@@ -251,17 +272,18 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
     if (ok) {
       const uint32_t lane_addr = tmem_acc + (uint32_t(sub * 32) << 16);
       const int tmax = rows - tile_t * BN;           // valid token columns in this tile
-      if (EPI == kEpiClusterSplit || EPI == kEpiClusterPush) {
-        // stage this split's partial tile: red[row][BN+1] over the (drained) A stages
+      if (EPI == kEpiClusterSplit || EPI == kEpiClusterPush || EPI == kEpiClusterSwiglu) {
+        // stage this split's partial tile: red[row][kA*BN+1] over the (drained) A stages
         float* red = reinterpret_cast<float*>(sA);
         const int row = sub * 32 + lane;
+        constexpr int kW = C::kA * BN + 1;
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 16) {
+        for (int c0 = 0; c0 < C::kA * BN; c0 += 16) {
           uint32_t r[16];
           tmem_ld_x16(lane_addr + c0, r);
           tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) red[row * (BN + 1) + c0 + j] = nk > 0 ? __uint_as_float(r[j]) : 0.f;
+          for (int j = 0; j < 16; ++j) red[row * kW + c0 + j] = nk > 0 ? __uint_as_float(r[j]) : 0.f;
         }
       } else if (EPI == kEpiStoreBf16 || EPI == kEpiAtomicF32 || EPI == kEpiWeightedBf16) {
 #pragma unroll 1
@@ -320,12 +342,15 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
 
   tc_fence_before();
   __syncthreads();
-  if constexpr (EPI == kEpiClusterSplit || EPI == kEpiClusterPush) {
+  if constexpr (EPI == kEpiClusterSplit || EPI == kEpiClusterPush || EPI == kEpiClusterSwiglu) {
     // Every split of this output tile has staged its partial; CTA `rank`
     // sums rows [rank*RPC, (rank+1)*RPC) of the tile across the cluster.
     // kEpiClusterPush stores the sums into recv[parity][my rank] of every
-    // rank (P2P over NVLink) and then publishes with one counter increment
-    // per rank, so the all-reduce transfer overlaps the remaining tiles.
+    // rank (P2P over NVLink, 16-byte stores) and then publishes with one
+    // counter increment per rank, so the all-reduce transfer overlaps the
+    // remaining tiles.  kEpiClusterSwiglu applies SwiGLU to the summed gate
+    // and up rows and requantizes to MXFP8 (one warp = one 32-channel block).
+    constexpr int kW = C::kA * BN + 1;
     const int parity = (EPI == kEpiClusterPush) ? int(__ldcg(p.ar_epoch) & 1u) : 0;
     cluster_sync();
     const int S = gridDim.z;
@@ -333,23 +358,54 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
     const int rpc = kTileM / S;
     const uint32_t red_local = smem_u32(sA);
     const int tmax = rows - tile_t * BN;
-    for (int i = threadIdx.x; i < rpc * BN; i += kThreads) {
-      const int rr = rank * rpc + (i % rpc);
-      const int col = i / rpc;
-      if (col < tmax) {
-        const uint32_t off = (uint32_t)(rr * (BN + 1) + col) * 4u;
-        float acc = 0.f;
-        for (int q = 0; q < S; ++q) acc += ld_dsmem_f32(mapa_shared(red_local + off, q));
-        const __nv_bfloat16 v = __float2bfloat16(acc);
-        const int64_t oi = (int64_t)(b_row + col) * p.ldo + tile_n * kTileM + rr;
+    if constexpr (EPI == kEpiClusterSwiglu) {
+      const int blocks = rpc / 32;
+      for (int wi = warp; wi < BN * blocks; wi += kThreads / 32) {
+        const int col = wi / blocks;
+        if (col >= tmax) continue;                     // uniform per warp
+        const int rr = rank * rpc + (wi % blocks) * 32 + lane;
+        float g = 0.f, u = 0.f;
+        for (int q = 0; q < S; ++q) {
+          g += ld_dsmem_f32(mapa_shared(red_local + (uint32_t)(rr * kW + col) * 4u, q));
+          u += ld_dsmem_f32(mapa_shared(red_local + (uint32_t)(rr * kW + BN + col) * 4u, q));
+        }
+        const float h = g / (1.0f + __expf(-g)) * u;
+        float amax = fabsf(h);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const int ex = ceil_log2_bits(amax * (1.0f / 448.0f));
+        const int orow = b_row + col;
+        const int ch = tile_n * kTileM + rr;
+        p.q_out[(int64_t)orow * p.ldq + ch] = uint8_t(f2_to_e4m3x2(h * exp2_int(-ex), 0.f) & 0xFF);
+        if (lane == 0) p.sf_out[sf_offset(orow, ch >> 5, p.ldq / 32)] = uint8_t(ex + 127);
+      }
+    } else {
+      // 8 consecutive output channels per work item -> one 16-byte store
+      const int groups = rpc / 8;
+      for (int i = threadIdx.x; i < groups * BN; i += kThreads) {
+        const int col = i / groups;
+        if (col >= tmax) continue;
+        const int rr0 = rank * rpc + (i % groups) * 8;
+        float acc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+        for (int q = 0; q < S; ++q) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[j] += ld_dsmem_f32(mapa_shared(red_local + (uint32_t)((rr0 + j) * kW + col) * 4u, q));
+        }
+        uint4 v;
+        __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&v);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) h2[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+        const int64_t oi = (int64_t)(b_row + col) * p.ldo + tile_n * kTileM + rr0;
         if constexpr (EPI == kEpiClusterPush) {
           for (int dst = 0; dst < p.peers.world; ++dst) {
             __nv_bfloat16* slot = reinterpret_cast<__nv_bfloat16*>(p.peers.base[dst] + kArRecvOff) +
                                   ((int64_t)(parity * p.peers.world + p.peers.rank) * p.peers.max_t) * p.ldo;
-            slot[oi] = v;
+            *reinterpret_cast<uint4*>(slot + oi) = v;
           }
         } else {
-          reinterpret_cast<__nv_bfloat16*>(p.out)[oi] = v;
+          *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + oi) = v;
         }
       }
     }
@@ -365,7 +421,6 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
     }
     cluster_sync();
   }
-  if (warp == 0 && lane == 0) pdl_launch_dependents();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, C::kTmemCols);
@@ -438,7 +493,7 @@ static int launch_t(const GemmArgs& a, cudaStream_t st) {
   auto kern = gemm_mxf8_kernel<BN, EPI, GROUPED>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   dim3 grid;
-  grid.x = (EPI == kEpiSwiglu ? a.inter : a.nw) / kTileM;
+  grid.x = (C::kGateUp ? a.inter : a.nw) / kTileM;
   grid.y = GROUPED ? (a.max_rows_per_expert + BN - 1) / BN : (a.t + BN - 1) / BN;
   grid.z = GROUPED ? a.num_experts : splits;
   if (grid.y == 0) return 0;
@@ -451,7 +506,7 @@ static int launch_t(const GemmArgs& a, cudaStream_t st) {
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = a.pdl ? 1 : 0;
   int nattr = 1;
-  if (EPI == kEpiClusterSplit || EPI == kEpiClusterPush) {
+  if (C::kCluster) {
     attr[1].id = cudaLaunchAttributeClusterDimension;
     attr[1].val.clusterDim.x = 1;
     attr[1].val.clusterDim.y = 1;
@@ -470,7 +525,7 @@ static int launch_bn(const GemmArgs& a, cudaStream_t st) {
   if (t <= 16) return launch_t<16, EPI, GROUPED>(a, st);
   if (t <= 32) return launch_t<32, EPI, GROUPED>(a, st);
   if (t <= 64) return launch_t<64, EPI, GROUPED>(a, st);
-  if constexpr (EPI == kEpiSwiglu) {
+  if constexpr (EPI == kEpiSwiglu || EPI == kEpiClusterSwiglu) {
     return launch_t<128, EPI, GROUPED>(a, st);
   } else {
     if (t <= 128) return launch_t<128, EPI, GROUPED>(a, st);
@@ -495,6 +550,9 @@ int b200_gemm_mxf8(const GemmArgs* a, cudaStream_t st) {
     case kEpiClusterPush:
       if (g || a->splits < 2 || a->splits > 8 || (128 % a->splits) != 0 || a->t > 128 || !a->ar_peers) return -14;
       return launch_bn<kEpiClusterPush, false>(*a, st);
+    case kEpiClusterSwiglu:
+      if (g || a->splits < 2 || a->splits > 4 || a->t > 128 || a->inter % 128) return -15;
+      return launch_bn<kEpiClusterSwiglu, false>(*a, st);
   }
   return -12;
 }

@@ -11,6 +11,8 @@ enum GemmEpi : int {
   kEpiClusterSplit = 4,  // split-K over a thread-block cluster, DSMEM reduction, bf16 out
   kEpiClusterPush = 5,   // as kEpiClusterSplit, but the reduced tile is pushed into every
                          // rank's all-reduce receive slot (fused GEMM + all-reduce)
+  kEpiClusterSwiglu = 6, // split-K over a cluster for thin gate_up GEMMs; the reduce applies
+                         // SwiGLU and MXFP8 requant (q_out / sf_out)
 };
 
 struct GemmArgs {

@@ -98,14 +98,14 @@ def test_gemm_splitk_fp32():
     assert rel_err(out, exp) < 1e-4
 
 
-@pytest.mark.parametrize("T", [1, 20, 64, 200])
-def test_gemm_swiglu_quant(T):
+@pytest.mark.parametrize("T,splits", [(1, 1), (20, 1), (64, 1), (200, 1), (1, 4), (20, 2), (64, 4), (128, 2)])
+def test_gemm_swiglu_quant(T, splits):
     from b200ds.ops import QAct, cuda, ref
     from b200ds.ops.quant import dequant_mxfp8
     K, I = 1024, 256
     a = _mx(torch.randn(T, K, device=DEV))
     wq = _mx(torch.randn(2 * I, K, device=DEV) * 0.05)
-    o = cuda.gemm_swiglu_quant(QAct(a.data, a.sf), wq)
+    o = cuda.gemm_swiglu_quant(QAct(a.data, a.sf), wq, splits=splits)
     y = ref.swiglu(ref.gemm_mxfp8(a.data, a.sf, wq.data, wq.sf))
     assert rel_err(dequant_mxfp8(o.q, o.sf)[:T], y) < 4e-2
 
