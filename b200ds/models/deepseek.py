@@ -192,10 +192,17 @@ class DeepseekModel:
         mw: MoEWeights = lw.ffn
         w, ids = ops.router(h, mw.gate, mw.bias, c)
         if fuse and ops.get_impl() == "native":
+            # The shared expert is independent of the routed experts: run it on
+            # a side stream (a parallel branch of the captured graph) while the
+            # routing + grouped GEMMs run on the main stream.
+            shared = None
+            if mw.shared_gate_up is not None:
+                shared = self._fork(lambda: lw.ffn.shared_down(ops.gate_up_swiglu(h, mw.shared_gate_up),
+                                                               out_dtype=out_dt), h)
             part = ops.moe_experts(h, w, ids, mw.experts, out_dtype=out_dt, n_experts_total=c.n_routed_experts,
                                    combine=False)
-            if mw.shared_gate_up is not None:
-                part.add = lw.ffn.shared_down(ops.gate_up_swiglu(h, mw.shared_gate_up), out_dtype=out_dt)
+            if shared is not None:
+                part.add = self._join(shared)
             return part
         out = ops.moe_experts(h, w, ids, mw.experts, out_dtype=out_dt, n_experts_total=c.n_routed_experts)
         if mw.shared_gate_up is not None:
@@ -204,6 +211,28 @@ class DeepseekModel:
         return out
 
     # ------------------------------------------------------------------
+    def _fork(self, fn, *inputs):
+        """Run fn() on the side stream after the main stream's pending work;
+        returns a handle for `_join`."""
+        main = torch.cuda.current_stream(self.device)
+        if getattr(self, "_side", None) is None:
+            self._side = torch.cuda.Stream(device=self.device)
+        side = self._side
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            out = fn()
+        for t in inputs:
+            for x in ((t.q, t.sf, t.hf) if isinstance(t, ops.QAct) else (t,)):
+                if isinstance(x, torch.Tensor):
+                    x.record_stream(side)
+        return out
+
+    def _join(self, out):
+        main = torch.cuda.current_stream(self.device)
+        main.wait_stream(self._side)
+        out.record_stream(main)
+        return out
+
     @torch.no_grad()
     def forward(self, fb: ForwardBatch) -> torch.Tensor:
         """Returns logits [B, V] (full vocab) for each sequence's last token."""

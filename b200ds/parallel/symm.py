@@ -39,7 +39,8 @@ class FusedAllReduce:
         self.hdl = symm_mem.rendezvous(self.buf, name)
         self.bases = [int(p) for p in self.hdl.buffer_ptrs]
         self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.ticket = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.ticket = torch.zeros(1, dtype=torch.int32, device=dev)        # reduce-side ticket
+        self.push_ticket = torch.zeros(1, dtype=torch.int32, device=dev)   # push-side ticket
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
         torch.cuda.synchronize(dev)
         dist.barrier(group=group)
@@ -54,10 +55,10 @@ class FusedAllReduce:
         from ..ops.cuda import alloc_qact
         T, H = a.shape
         x = a if (a.dtype == torch.bfloat16 and a.is_contiguous()) else a.to(torch.bfloat16).contiguous()
-        _C.ar_push(x, self.bases, self.rank, self.max_tokens, self.epoch, self.push_ctas)
+        _C.ar_push(x, self.bases, self.rank, self.max_tokens, self.epoch, self.push_ticket, self.push_ctas)
         y = torch.empty(T, H, dtype=torch.bfloat16, device=a.device) if (keep_bf16 or not quantize) else None
         qa = alloc_qact(T, H, a.device) if quantize else None
-        _C.ar_reduce_norm(T, H, self.bases, self.rank, self.max_tokens, self.epoch, self.ticket, self.push_ctas,
+        _C.ar_reduce_norm(T, H, self.bases, self.rank, self.max_tokens, self.epoch, self.ticket, 1,
                           residual, w, eps, y, qa.q if qa else None, qa.sf if qa else None, self.err)
         if qa is not None:
             qa.hf = y
@@ -93,7 +94,7 @@ class FusedAllReduce:
             from ..ops.cuda import gemm
             return self.allreduce_add_rmsnorm(gemm(a, wq), residual, ln_w, eps, quantize)
         n = _C.gemm_push(wq.data, wq.sf, a.q, a.sf, N, T, K, splits, self.bases, self.rank, self.max_tokens,
-                         self.epoch)
+                         self.epoch, self.push_ticket)
         y, qa = self._outs(T, N, a.q.device, quantize)
         return self._reduce(T, N, int(n), residual, ln_w, eps, y, qa)
 
@@ -105,9 +106,9 @@ class FusedAllReduce:
         H = part.y.shape[1]
         add = part.add.to(torch.bfloat16).contiguous() if part.add is not None else None
         _C.moe_combine_push(part.y, part.pair_row, add, self.bases, self.rank, self.max_tokens, self.epoch,
-                            self.push_ctas)
+                            self.push_ticket, self.push_ctas)
         y, qa = self._outs(T, H, part.y.device, quantize)
-        return self._reduce(T, H, self.push_ctas, residual, ln_w, eps, y, qa)
+        return self._reduce(T, H, 1, residual, ln_w, eps, y, qa)
 
     def check(self) -> None:
         """Raise if a bounded wait inside the kernels timed out."""

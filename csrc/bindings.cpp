@@ -103,7 +103,7 @@ void gemm(const at::Tensor& w, const at::Tensor& w_sf, int64_t w_sf_estride, con
 // Returns the number of CTAs that publish (the reduce kernel's expected count).
 int64_t gemm_push(const at::Tensor& w, const at::Tensor& w_sf, const at::Tensor& x, const at::Tensor& x_sf,
                   int64_t nw, int64_t t, int64_t k, int64_t splits, std::vector<int64_t> bases, int64_t rank,
-                  int64_t max_t, const at::Tensor& epoch) {
+                  int64_t max_t, const at::Tensor& epoch, at::Tensor ticket) {
   check_cuda(w, "w");
   const c10::cuda::CUDAGuard g(w.device());
   TORCH_CHECK(k % 128 == 0 && nw % 128 == 0, "k, nw multiples of 128");
@@ -128,10 +128,10 @@ int64_t gemm_push(const at::Tensor& w, const at::Tensor& w_sf, const at::Tensor&
   a.ldo = nw;
   a.ar_peers = &pe;
   a.ar_epoch = reinterpret_cast<const uint32_t*>(epoch.data_ptr());
+  a.ar_ticket = reinterpret_cast<uint32_t*>(ticket.data_ptr());
   a.pdl = 1;
   check(b200_gemm_mxf8(&a, cur_stream()), "gemm_push");
-  const int64_t bn = t <= 16 ? 16 : t <= 32 ? 32 : t <= 64 ? 64 : 128;
-  return (nw / 128) * ((t + bn - 1) / bn) * splits;
+  return 1;   // arrivals per source rank
 }
 
 void rope(at::Tensor x, const at::Tensor& pos, const at::Tensor& table) {

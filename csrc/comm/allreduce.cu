@@ -50,6 +50,26 @@ __device__ __forceinline__ int64_t sf_off(int row, int kblock, int kb_total) {
   return ((int64_t)(rb * (kb_total >> 2) + kc) << 9) + ((r & 31) << 4) + ((r >> 5) << 2) + c;
 }
 
+// Called by every CTA of a push grid after its peer stores: each CTA fences
+// and takes a local ticket; the last one publishes once per rank (one
+// system-scope increment per destination instead of one per CTA, which
+// serialised thousands of atomics on the same counter word).
+__device__ __forceinline__ void publish_push(const ArPeers& peers, int parity, uint32_t* ticket) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const uint32_t prev = atomicAdd(ticket, 1u);
+    if (prev == gridDim.x * gridDim.y * gridDim.z - 1) {
+      __threadfence_system();
+      *ticket = 0u;
+      for (int q = 0; q < peers.world; ++q)
+        asm volatile("red.release.sys.global.add.u32 [%0], %1;"
+                     ::"l"(reinterpret_cast<uint32_t*>(peers.base[q]) + parity * kArMaxRanks + peers.rank), "r"(1u)
+                     : "memory");
+    }
+  }
+}
+
 __device__ __forceinline__ uint32_t* counters(uint8_t* base, int parity) {
   return reinterpret_cast<uint32_t*>(base) + parity * kArMaxRanks;
 }
@@ -61,7 +81,7 @@ __device__ __forceinline__ __nv_bfloat16* recv_slot(uint8_t* base, int parity, i
 
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads) ar_push_kernel(const __nv_bfloat16* __restrict__ x, int T, int hidden,
-                                                           ArPeers peers, const uint32_t* epoch) {
+                                                           ArPeers peers, const uint32_t* epoch, uint32_t* ticket) {
   pdl_wait();
   if (threadIdx.x == 0) pdl_launch_dependents();   // e.g. the next GEMM prefetches weights during our wait
   const int p = (*epoch) & 1;
@@ -74,11 +94,7 @@ __global__ void __launch_bounds__(kThreads) ar_push_kernel(const __nv_bfloat16* 
     uint4* dst = reinterpret_cast<uint4*>(recv_slot(peers.base[q], p, peers.rank, peers.world, peers.max_t, hidden));
     for (int64_t v = v0 + threadIdx.x; v < v1; v += blockDim.x) dst[v] = src[v];
   }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    for (int q = 0; q < peers.world; ++q) red_release_sys_add(counters(peers.base[q], p) + peers.rank, 1u);
-  }
+  publish_push(peers, p, ticket);
 }
 
 // ---------------------------------------------------------------------------
@@ -214,12 +230,12 @@ __global__ void __launch_bounds__(kThreads) ar_reduce_norm_kernel(
 }  // namespace comm
 }  // namespace b200
 
-int b200_ar_push(const void* x, int T, int hidden, const ArPeers* peers, const uint32_t* epoch, int nctas,
-                 cudaStream_t st) {
+int b200_ar_push(const void* x, int T, int hidden, const ArPeers* peers, const uint32_t* epoch, uint32_t* ticket,
+                 int nctas, cudaStream_t st) {
   if (T <= 0) return 0;
   if (T > peers->max_t || hidden % 8 || peers->world > kArMaxRanks || nctas <= 0) return -1;
   b200::comm::ar_push_kernel<<<nctas, b200::comm::kThreads, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(x), T,
-                                                                      hidden, *peers, epoch);
+                                                                      hidden, *peers, epoch, ticket);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
 
@@ -244,7 +260,7 @@ namespace comm {
 __global__ void __launch_bounds__(kThreads) moe_combine_push_kernel(const __nv_bfloat16* __restrict__ y,
                                                                      const int* __restrict__ pair_row, int T, int K,
                                                                      int hidden, const __nv_bfloat16* __restrict__ add,
-                                                                     ArPeers peers, const uint32_t* epoch) {
+                                                                     ArPeers peers, const uint32_t* epoch, uint32_t* ticket) {
   pdl_wait();
   if (threadIdx.x == 0) pdl_launch_dependents();   // e.g. the next GEMM prefetches weights during our wait
   const int p = (*epoch) & 1;
@@ -289,21 +305,17 @@ __global__ void __launch_bounds__(kThreads) moe_combine_push_kernel(const __nv_b
       *reinterpret_cast<uint4*>(dst + (int64_t)t * hidden + c) = outv;
     }
   }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    for (int q = 0; q < peers.world; ++q) red_release_sys_add(counters(peers.base[q], p) + peers.rank, 1u);
-  }
+  publish_push(peers, p, ticket);
 }
 }  // namespace comm
 }  // namespace b200
 
 int b200_moe_combine_push(const void* y, const int* pair_row, int T, int K, int hidden, const void* add,
-                          const ArPeers* peers, const uint32_t* epoch, int nctas, cudaStream_t st) {
+                          const ArPeers* peers, const uint32_t* epoch, uint32_t* ticket, int nctas, cudaStream_t st) {
   if (T <= 0) return 0;
   if (T > peers->max_t || hidden % 8 || nctas <= 0) return -1;
   b200::comm::moe_combine_push_kernel<<<nctas, b200::comm::kThreads, 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(y), pair_row, T, K, hidden, reinterpret_cast<const __nv_bfloat16*>(add),
-      *peers, epoch);
+      *peers, epoch, ticket);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }

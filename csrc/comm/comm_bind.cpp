@@ -23,12 +23,13 @@ T* optr(const c10::optional<at::Tensor>& t) {
 }
 
 void ar_push(const at::Tensor& x, std::vector<int64_t> bases, int64_t rank, int64_t max_t, const at::Tensor& epoch,
-             int64_t nctas) {
+             at::Tensor ticket, int64_t nctas) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() == 2, "x bf16 [T,H]");
   const c10::cuda::CUDAGuard g(x.device());
   ArPeers p = make_peers(bases, rank, max_t);
   const int rc = b200_ar_push(x.data_ptr(), x.size(0), x.size(1), &p, reinterpret_cast<const uint32_t*>(epoch.data_ptr()),
-                              nctas, at::cuda::getCurrentCUDAStream().stream());
+                              reinterpret_cast<uint32_t*>(ticket.data_ptr()), nctas,
+                              at::cuda::getCurrentCUDAStream().stream());
   TORCH_CHECK(rc == 0, "ar_push failed ", rc);
 }
 
@@ -49,7 +50,8 @@ void ar_reduce_norm(int64_t T, int64_t hidden, std::vector<int64_t> bases, int64
 }
 
 void moe_combine_push(const at::Tensor& y, const at::Tensor& pair_row, c10::optional<at::Tensor> add,
-                      std::vector<int64_t> bases, int64_t rank, int64_t max_t, const at::Tensor& epoch, int64_t nctas) {
+                      std::vector<int64_t> bases, int64_t rank, int64_t max_t, const at::Tensor& epoch,
+                      at::Tensor ticket, int64_t nctas) {
   TORCH_CHECK(y.is_cuda() && y.scalar_type() == at::kBFloat16 && y.is_contiguous(), "y bf16");
   TORCH_CHECK(pair_row.scalar_type() == at::kInt && pair_row.is_contiguous(), "pair_row int32 [T,K]");
   if (add.has_value()) TORCH_CHECK(add->scalar_type() == at::kBFloat16 && add->is_contiguous(), "add bf16 [T,H]");
@@ -57,7 +59,8 @@ void moe_combine_push(const at::Tensor& y, const at::Tensor& pair_row, c10::opti
   ArPeers p = make_peers(bases, rank, max_t);
   const int rc = b200_moe_combine_push(y.data_ptr(), reinterpret_cast<const int*>(pair_row.data_ptr()), pair_row.size(0),
                                        pair_row.size(1), y.size(1), optr<void>(add), &p,
-                                       reinterpret_cast<const uint32_t*>(epoch.data_ptr()), nctas,
+                                       reinterpret_cast<const uint32_t*>(epoch.data_ptr()),
+                                       reinterpret_cast<uint32_t*>(ticket.data_ptr()), nctas,
                                        at::cuda::getCurrentCUDAStream().stream());
   TORCH_CHECK(rc == 0, "moe_combine_push failed ", rc);
 }

@@ -84,6 +84,7 @@ struct Params {
   uint32_t* err;
   ArPeers peers;             // kEpiClusterPush
   const uint32_t* ar_epoch;
+  uint32_t* ar_ticket;
 };
 
 // Byte offset of the scale byte for (row, kblock) inside a packed sf128x4
@@ -410,12 +411,18 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
       }
     }
     if constexpr (EPI == kEpiClusterPush) {
+      // every CTA fences + takes a ticket; the last publishes once per rank
       __syncthreads();
       if (threadIdx.x == 0) {
         __threadfence_system();
-        for (int dst = 0; dst < p.peers.world; ++dst) {
-          uint32_t* cnt = reinterpret_cast<uint32_t*>(p.peers.base[dst]) + parity * kArMaxRanks + p.peers.rank;
-          asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(cnt), "r"(1u) : "memory");
+        const uint32_t prev = atomicAdd(p.ar_ticket, 1u);
+        if (prev == gridDim.x * gridDim.y * gridDim.z - 1) {
+          __threadfence_system();
+          *p.ar_ticket = 0u;
+          for (int dst = 0; dst < p.peers.world; ++dst) {
+            uint32_t* cnt = reinterpret_cast<uint32_t*>(p.peers.base[dst]) + parity * kArMaxRanks + p.peers.rank;
+            asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(cnt), "r"(1u) : "memory");
+          }
         }
       }
     }
@@ -489,6 +496,7 @@ static int launch_t(const GemmArgs& a, cudaStream_t st) {
   if (EPI == kEpiClusterPush) {
     p.peers = *reinterpret_cast<const ArPeers*>(a.ar_peers);
     p.ar_epoch = a.ar_epoch;
+    p.ar_ticket = a.ar_ticket;
   }
   auto kern = gemm_mxf8_kernel<BN, EPI, GROUPED>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);

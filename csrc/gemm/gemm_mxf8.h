@@ -44,6 +44,7 @@ struct GemmArgs {
   // kEpiClusterPush: symmetric all-reduce buffers (see comm/comm.h)
   const void* ar_peers;     // const ArPeers*
   const uint32_t* ar_epoch;
+  uint32_t* ar_ticket;      // publish ticket (last CTA publishes)
 };
 
 int b200_gemm_mxf8(const GemmArgs* args, cudaStream_t stream);
