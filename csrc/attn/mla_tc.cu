@@ -474,10 +474,10 @@ static int launch(const MlaTcArgs& a, cudaStream_t st) {
   auto kern = mla_tc_kernel<HB>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes);
   dim3 grid(a.T, a.H / HB, a.nsplit);
-  kern<<<grid, kThreads, S::kBytes, st>>>(mql, mqr, mkl, mkr, p);
+  b200::launch_pdl(kern, dim3(grid), dim3(kThreads), S::kBytes, st, mql, mqr, mkl, mkr, p);
   if (cudaGetLastError() != cudaSuccess) return 1;
   if (a.nsplit > 1) {
-    mla_merge_kernel<<<a.T * a.H, 128, 0, st>>>(a.part_o, a.part_lse, a.nsplit, a.T * a.H,
+    b200::launch_pdl(mla_merge_kernel, dim3(a.T * a.H), dim3(128), 0, st, a.part_o, a.part_lse, a.nsplit, a.T * a.H,
                                                  reinterpret_cast<__nv_bfloat16*>(a.out));
     if (cudaGetLastError() != cudaSuccess) return 2;
   }
@@ -489,7 +489,7 @@ static int launch(const MlaTcArgs& a, cudaStream_t st) {
 
 int b200_mla_q_quant(const void* q_abs, const void* q_pe, int TH, uint8_t* q8, float* qs, cudaStream_t st) {
   if (TH <= 0) return 0;
-  b200::mla::q_quant_kernel<<<(TH * 32 + 127) / 128, 128, 0, st>>>(
+  b200::launch_pdl(b200::mla::q_quant_kernel, dim3((TH * 32 + 127) / 128), dim3(128), 0, st, 
       reinterpret_cast<const __nv_bfloat16*>(q_abs), reinterpret_cast<const __nv_bfloat16*>(q_pe), TH, q8, qs);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }

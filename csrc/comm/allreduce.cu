@@ -234,7 +234,7 @@ int b200_ar_push(const void* x, int T, int hidden, const ArPeers* peers, const u
                  int nctas, cudaStream_t st) {
   if (T <= 0) return 0;
   if (T > peers->max_t || hidden % 8 || peers->world > kArMaxRanks || nctas <= 0) return -1;
-  b200::comm::ar_push_kernel<<<nctas, b200::comm::kThreads, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(x), T,
+  b200::launch_pdl(b200::comm::ar_push_kernel, dim3(nctas), dim3(b200::comm::kThreads), 0, st, reinterpret_cast<const __nv_bfloat16*>(x), T,
                                                                       hidden, *peers, epoch, ticket);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
@@ -244,7 +244,7 @@ int b200_ar_reduce_norm(int T, int hidden, const ArPeers* peers, uint32_t* epoch
                         cudaStream_t st) {
   if (T <= 0) return 0;
   if (T > peers->max_t || hidden % 32 || hidden > b200::comm::kThreads * 8 * b200::comm::kMaxIt) return -1;
-  b200::comm::ar_reduce_norm_kernel<<<T, b200::comm::kThreads, 0, st>>>(
+  b200::launch_pdl(b200::comm::ar_reduce_norm_kernel, dim3(T), dim3(b200::comm::kThreads), 0, st, 
       T, hidden, *peers, epoch, ticket, (uint32_t)push_ctas, residual, w, eps,
       reinterpret_cast<__nv_bfloat16*>(y), q, sf, err);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
@@ -314,7 +314,7 @@ int b200_moe_combine_push(const void* y, const int* pair_row, int T, int K, int 
                           const ArPeers* peers, const uint32_t* epoch, uint32_t* ticket, int nctas, cudaStream_t st) {
   if (T <= 0) return 0;
   if (T > peers->max_t || hidden % 8 || nctas <= 0) return -1;
-  b200::comm::moe_combine_push_kernel<<<nctas, b200::comm::kThreads, 0, st>>>(
+  b200::launch_pdl(b200::comm::moe_combine_push_kernel, dim3(nctas), dim3(b200::comm::kThreads), 0, st, 
       reinterpret_cast<const __nv_bfloat16*>(y), pair_row, T, K, hidden, reinterpret_cast<const __nv_bfloat16*>(add),
       *peers, epoch, ticket);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;

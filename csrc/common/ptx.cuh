@@ -342,3 +342,25 @@ B200_DEVICE float ld_dsmem_f32(uint32_t cluster_addr) {
   return v;
 }
 }  // namespace b200
+
+namespace b200 {
+// Launch with programmatic stream serialization: the kernel may start while
+// the previous kernel in the stream drains; every kernel of this project
+// executes griddepcontrol.wait before it reads its predecessor's outputs or
+// writes anything, and triggers its own dependents at entry.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+}  // namespace b200

@@ -177,13 +177,13 @@ int b200_rmsnorm(const void* x, int x_is_f32, int ldx, float* residual, const fl
   dim3 grid(rows), block(kThreads);
   __nv_bfloat16* yb = reinterpret_cast<__nv_bfloat16*>(y);
   if (residual) {
-    rmsnorm_kernel<__nv_bfloat16, 1><<<grid, block, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx,
+    b200::launch_pdl(rmsnorm_kernel<__nv_bfloat16, 1>, dim3(grid), dim3(block), 0, st, reinterpret_cast<const __nv_bfloat16*>(x), ldx,
                                                               residual, w, eps, K, yb, ldy, q, sf);
   } else if (x_is_f32) {
-    rmsnorm_kernel<float, 0><<<grid, block, 0, st>>>(reinterpret_cast<const float*>(x), ldx, nullptr, w, eps, K,
+    b200::launch_pdl(rmsnorm_kernel<float, 0>, dim3(grid), dim3(block), 0, st, reinterpret_cast<const float*>(x), ldx, nullptr, w, eps, K,
                                                       yb, ldy, q, sf);
   } else {
-    rmsnorm_kernel<__nv_bfloat16, 0><<<grid, block, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx,
+    b200::launch_pdl(rmsnorm_kernel<__nv_bfloat16, 0>, dim3(grid), dim3(block), 0, st, reinterpret_cast<const __nv_bfloat16*>(x), ldx,
                                                               nullptr, w, eps, K, yb, ldy, q, sf);
   }
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
@@ -194,8 +194,8 @@ int b200_quant_mxfp8(const void* x, int x_is_f32, int ldx, int rows, int K, uint
   if (K % 128 != 0 || rows <= 0) return -1;
   dim3 grid((K / 8 + kThreads - 1) / kThreads, rows), block(kThreads);
   if (x_is_f32)
-    quant_kernel<float><<<grid, block, 0, st>>>(reinterpret_cast<const float*>(x), ldx, K, q, sf);
+    b200::launch_pdl(quant_kernel<float>, dim3(grid), dim3(block), 0, st, reinterpret_cast<const float*>(x), ldx, K, q, sf);
   else
-    quant_kernel<__nv_bfloat16><<<grid, block, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, K, q, sf);
+    b200::launch_pdl(quant_kernel<__nv_bfloat16>, dim3(grid), dim3(block), 0, st, reinterpret_cast<const __nv_bfloat16*>(x), ldx, K, q, sf);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }

@@ -289,7 +289,7 @@ using namespace b200::ew2;
 int b200_rope(void* x, int f32, int64_t st_t, int64_t st_h, int T, int H, int d, const int* pos, const float* table,
               cudaStream_t st) {
   if (T <= 0) return 0;
-  rope_kernel<<<T, 128, 0, st>>>(x, f32, st_t, st_h, H, d, pos, table);
+  b200::launch_pdl(rope_kernel, dim3(T), dim3(128), 0, st, x, f32, st_t, st_h, H, d, pos, table);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
 
@@ -299,7 +299,7 @@ int b200_kv_store(const void* kv, int f32, int64_t ld, int T, int L, int R, cons
   if (L % 64 != 0) return -1;
   const int threads = 128;
   const int blocks = (T * 32 + threads - 1) / threads;
-  kv_store_kernel<<<blocks, threads, 0, st>>>(kv, f32, ld, T, L, R, w, eps, pos, table, slots, cache, 1.0f / kv_scale);
+  b200::launch_pdl(kv_store_kernel, dim3(blocks), dim3(threads), 0, st, kv, f32, ld, T, L, R, w, eps, pos, table, slots, cache, 1.0f / kv_scale);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
 
@@ -308,7 +308,7 @@ int b200_router(const float* logits, const float* bias, int T, int E, int G, int
   if (T <= 0) return 0;
   if (E % 32 != 0 || E / 32 > kMaxEPerLane || K > 32 || (G > 1 && (32 % G != 0))) return -1;
   const int threads = 128;
-  router_kernel<<<(T * 32 + threads - 1) / threads, threads, 0, st>>>(logits, bias, T, E, G, topk_group, K, scaling,
+  b200::launch_pdl(router_kernel, dim3((T * 32 + threads - 1) / threads), dim3(threads), 0, st, logits, bias, T, E, G, topk_group, K, scaling,
                                                                        renorm, w_out, id_out);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
@@ -316,7 +316,7 @@ int b200_router(const float* logits, const float* bias, int T, int E, int G, int
 int b200_moe_align(const int* ids, const float* w, int T, int K, int first, int E, int* seg_start, int* seg_count,
                    int* row_token, float* row_weight, int* pair_row, int* total_rows, int bn1, int* ttile1, int bn2,
                    int* ttile2, cudaStream_t st) {
-  moe_align_kernel<<<1, 1024, 3 * E * sizeof(int), st>>>(ids, w, T, K, first, E, seg_start, seg_count, row_token,
+  b200::launch_pdl(moe_align_kernel, dim3(1), dim3(1024), 3 * E * sizeof(int), st, ids, w, T, K, first, E, seg_start, seg_count, row_token,
                                                          row_weight, pair_row, total_rows, bn1 > 0 ? bn1 : 128, ttile1,
                                                          bn2 > 0 ? bn2 : 128, ttile2);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
@@ -325,14 +325,14 @@ int b200_moe_align(const int* ids, const float* w, int T, int K, int first, int 
 int b200_moe_gather(const uint8_t* xq, const uint8_t* xsf, const int* pair_row, int npairs, int K, int Kd, uint8_t* dq,
                     uint8_t* dsf, cudaStream_t st) {
   if (npairs <= 0) return 0;
-  moe_gather_kernel<<<npairs, 128, 0, st>>>(xq, xsf, pair_row, npairs, K, Kd, dq, dsf);
+  b200::launch_pdl(moe_gather_kernel, dim3(npairs), dim3(128), 0, st, xq, xsf, pair_row, npairs, K, Kd, dq, dsf);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
 
 int b200_moe_combine(const void* y, const int* pair_row, int T, int K, int D, const void* add, int add_f32, void* out,
                      int out_f32, cudaStream_t st) {
   if (T <= 0) return 0;
-  moe_combine_kernel<<<T, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(y), pair_row, T, K, D, add, add_f32,
+  b200::launch_pdl(moe_combine_kernel, dim3(T), dim3(256), 0, st, reinterpret_cast<const __nv_bfloat16*>(y), pair_row, T, K, D, add, add_f32,
                                         out, out_f32);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }

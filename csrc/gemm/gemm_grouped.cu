@@ -76,18 +76,22 @@ struct Tile {
 
 // Tiles are ordered (expert, token tile) major, output-row tile minor, so
 // CTAs running at the same time share the expert's activation rows in L2.
-__device__ __forceinline__ Tile map_tile(const Params& p, int w) {
+// The routing layout (tile offsets, segment starts / counts) is staged in
+// shared memory once per CTA: sm_lay[0..E] = ttile_off, [E+1..2E] =
+// seg_start, [2E+1..3E] = seg_count.
+constexpr int kMaxExperts = 256;
+__device__ __forceinline__ Tile map_tile(const Params& p, const int* lay, int w) {
   const int ttg = w / p.n_tiles;
   Tile t;
   t.tile_n = w - ttg * p.n_tiles;
   int lo = 0, hi = p.E;   // e with ttile_off[e] <= ttg < ttile_off[e+1]
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
-    if (__ldcg(p.ttile_off + mid) <= ttg) lo = mid; else hi = mid;
+    if (lay[mid] <= ttg) lo = mid; else hi = mid;
   }
   t.e = lo;
-  t.tt = ttg - __ldcg(p.ttile_off + lo);
-  t.rows = __ldcg(p.seg_count + lo);
+  t.tt = ttg - lay[lo];
+  t.rows = lay[2 * p.E + 1 + lo];
   return t;
 }
 
@@ -106,6 +110,7 @@ grouped_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
   uint64_t* acc_full = empty + C::kStages;    // [2]
   uint64_t* acc_empty = acc_full + 2;         // [2]
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  __shared__ int lay[3 * kMaxExperts + 1];
 
   const int warp = warp_id(), lane = lane_id();
   if (threadIdx.x == 0) {
@@ -135,7 +140,13 @@ grouped_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
 
   pdl_wait();
   if (threadIdx.x == 0) pdl_launch_dependents();   // dependents wait for this grid's completion
-  const int total = __ldcg(p.ttile_off + p.E) * p.n_tiles;
+  for (int i = threadIdx.x; i <= p.E; i += blockDim.x) lay[i] = __ldcg(p.ttile_off + i);
+  for (int i = threadIdx.x; i < p.E; i += blockDim.x) {
+    lay[p.E + 1 + i] = __ldcg(p.seg_start + i);
+    lay[2 * p.E + 1 + i] = __ldcg(p.seg_count + i);
+  }
+  __syncthreads();
+  const int total = lay[p.E] * p.n_tiles;
   const int nk = p.k / kTileK;
   const int kc_total = p.k / kTileK;           // 512-byte sf chunks per 128 rows
 
@@ -148,10 +159,10 @@ grouped_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
       int it = 0;
       bool ok = true;
       for (int w = blockIdx.x; ok && w < total; w += gridDim.x) {
-        const Tile t = map_tile(p, w);
+        const Tile t = map_tile(p, lay, w);
         const int e = t.e;
         const int a_row = e * p.nw + t.tile_n * kTileM;
-        const int b_row = __ldcg(p.seg_start + e) + t.tt * BN;
+        const int b_row = lay[p.E + 1 + e] + t.tt * BN;
         const uint8_t* sfa_e = p.sfa + (int64_t)e * p.sfa_estride;
         for (int kt = 0; kt < nk; ++kt, ++it) {
           const int s = it % C::kStages;
@@ -178,8 +189,8 @@ grouped_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
     int it = 0, c = 0;
     bool ok = true;
     for (int w = blockIdx.x; ok && w < total; w += gridDim.x, ++c) {
-      const Tile t = map_tile(p, w);
-      const int b_row = __ldcg(p.seg_start + t.e) + t.tt * BN;
+      const Tile t = map_tile(p, lay, w);
+      const int b_row = lay[p.E + 1 + t.e] + t.tt * BN;
       const int buf = c & 1;
       if (c >= 2 && !mbar_wait(&acc_empty[buf], ((c >> 1) - 1) & 1, p.err)) { ok = false; break; }
       tc_fence_after();
@@ -235,11 +246,11 @@ grouped_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
     int c = 0;
     const int kb_out = p.ldq / 32;
     for (int w = blockIdx.x; w < total; w += gridDim.x, ++c) {
-      const Tile t = map_tile(p, w);
+      const Tile t = map_tile(p, lay, w);
       const int buf = c & 1;
       if (!mbar_wait(&acc_full[buf], (c >> 1) & 1, p.err)) break;
       tc_fence_after();
-      const int b_row = __ldcg(p.seg_start + t.e) + t.tt * BN;
+      const int b_row = lay[p.E + 1 + t.e] + t.tt * BN;
       const int tmax = t.rows - t.tt * BN;
       const int wrow = t.tile_n * kTileM + sub * 32 + lane;
       const uint32_t lane_addr = tmem + buf * C::kAcc + (uint32_t(sub * 32) << 16);
@@ -375,7 +386,7 @@ static int launch_bn(const GroupedArgs& a, cudaStream_t st) {
 
 int b200_gemm_grouped(const GroupedArgs* a, cudaStream_t st) {
   using namespace b200::ggemm;
-  if (a->k % 128 || a->nw % 128 || a->num_ctas <= 0) return -1;
+  if (a->k % 128 || a->nw % 128 || a->num_ctas <= 0 || a->E > b200::ggemm::kMaxExperts) return -1;
   if (a->epi == kEpiSwiglu) return launch_bn<kEpiSwiglu>(*a, st);
   if (a->epi == kEpiWeightedBf16) return launch_bn<kEpiWeightedBf16>(*a, st);
   return -5;
