@@ -64,12 +64,12 @@ class AttnWeights:
     w_uk: torch.Tensor            # [Hl, nope, kv_lora]
     w_uv: torch.Tensor            # [Hl, v, kv_lora]
     o_proj: Linear                # [h, Hl * v]
-    # sparse indexer (optional)
-    ix_wq_b: Optional[Linear] = None
-    ix_wk: Optional[torch.Tensor] = None
+    # Sparse indexer (optional).  Its projections ride on the attention GEMMs:
+    # qkv_a has [wk (index_head_dim); weights_proj (index_n_heads)] appended
+    # after the q_lora + kv rows, and q_b has the indexer's wq_b rows appended
+    # after this rank's q heads, so no extra GEMM launches are needed.
     ix_k_norm_w: Optional[torch.Tensor] = None
     ix_k_norm_b: Optional[torch.Tensor] = None
-    ix_weights: Optional[torch.Tensor] = None
 
 
 @dataclass
@@ -151,13 +151,13 @@ class DeepseekModel:
                                 keep_hf=bool(c.index_n_heads))
         ops.kv_store(qkv[:, ql:ql + c.kv_cache_dim], aw.kv_a_ln, c.rms_norm_eps, self.rope_table, fb.positions,
                      self.kv_cache[i], fb.out_slots, self.kv_scale[i], c.kv_lora_rank)
-        q = aw.q_b(q_lat, out_dtype=torch.float32 if self.device.type == "cpu" else torch.bfloat16)
-        q = q.view(T, self.heads, c.qk_head_dim)
+        qo = aw.q_b(q_lat, out_dtype=torch.float32 if self.device.type == "cpu" else torch.bfloat16)
+        q = qo[:, : self.heads * c.qk_head_dim].view(T, self.heads, c.qk_head_dim)
         q_pe = ops.rope(q[..., c.qk_nope_head_dim:], fb.positions, self.rope_table)
         q_abs = ops.absorb_q(q[..., : c.qk_nope_head_dim], aw.w_uk)       # [T, Hl, kv_lora]
         topk = None
         if c.index_n_heads:
-            topk = self._indexer(i, aw, h, q_lat, fb)
+            topk = self._indexer(i, aw, qkv, qo, fb)
         o_lat = ops.mla_attention(q_abs, q_pe, self.kv_cache[i], self.kv_scale[i], fb,
                                   c.softmax_scale, self.page_size, topk)
         o = ops.absorb_o(o_lat, aw.w_uv)                                  # [T, Hl*v]
@@ -166,19 +166,19 @@ class DeepseekModel:
             return ops.PendingLinear(o, aw.o_proj.w, aw.o_proj.out_features)
         return aw.o_proj(o, out_dtype=torch.float32 if self.device.type == "cpu" else torch.bfloat16)
 
-    def _indexer(self, i, aw: AttnWeights, h, q_lat, fb: ForwardBatch):
+    def _indexer(self, i, aw: AttnWeights, qkv, qo, fb: ForwardBatch):
+        """Lightning indexer: keys from the qkv_a GEMM's appended rows, queries
+        from q_b's appended rows; returns top-k cache positions [T, topk]."""
         c = self.cfg
-        T = fb.num_tokens
-        nh, hd, rd = c.index_n_heads, c.index_head_dim, c.qk_rope_head_dim
-        xf = ops.to_float(h)
-        q = aw.ix_wq_b(q_lat, out_dtype=torch.float32).view(T, nh, hd)
-        q = torch.cat([ops.rope(q[..., :rd], fb.positions, self.rope_table), q[..., rd:].float()], -1)
-        k = torch.nn.functional.layer_norm(xf @ aw.ix_wk.float().T, (hd,), aw.ix_k_norm_w.float(),
-                                           aw.ix_k_norm_b.float(), 1e-6)
-        k = torch.cat([ops.rope(k[:, :rd], fb.positions, self.rope_table), k[:, rd:]], -1)
-        ops.index_k_store(k, self.ix_cache[i], self.ix_scale[i], fb.out_slots)
-        wts = (xf @ aw.ix_weights.float().T) * (nh ** -0.5) * (hd ** -0.5)
-        return ops.indexer_topk(q, wts, self.ix_cache[i], self.ix_scale[i], fb, self.page_size, c.index_topk)
+        nh, hd = c.index_n_heads, c.index_head_dim
+        base = c.q_lora_rank + c.kv_cache_dim
+        k_raw = qkv[:, base: base + hd]
+        w_raw = qkv[:, base + hd: base + hd + nh]
+        q_raw = qo[:, self.heads * c.qk_head_dim: self.heads * c.qk_head_dim + nh * hd]
+        ops.index_k_store(k_raw, aw.ix_k_norm_w, aw.ix_k_norm_b, 1e-6, self.rope_table, fb.positions,
+                          self.ix_cache[i], self.ix_scale[i], fb.out_slots)
+        return ops.indexer_topk(q_raw, w_raw, (nh * hd) ** -0.5, self.rope_table, self.ix_cache[i],
+                                self.ix_scale[i], fb, self.page_size, c.index_topk)
 
     def _ffn(self, i: int, lw: LayerWeights, h, fb: ForwardBatch) -> torch.Tensor:
         c = self.cfg

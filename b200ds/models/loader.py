@@ -76,9 +76,16 @@ def build_model(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState,
         a = p + "self_attn."
         qa = get(a + "q_a_proj.weight")
         kva = get(a + "kv_a_proj_with_mqa.weight")
-        qkv_a = Linear(_quantize(torch.cat([qa, kva], 0), fmt_d, dev))
         qb = split(get(a + "q_b_proj.weight").view(H, cfg.qk_head_dim, -1), 0, attn_tp, attn_rank)
-        q_b = Linear(_quantize(qb.reshape(Hl * cfg.qk_head_dim, -1), fmt_d, dev))
+        qb = qb.reshape(Hl * cfg.qk_head_dim, -1)
+        a_rows, b_rows = [qa, kva], [qb]
+        if cfg.index_n_heads:
+            # indexer projections appended to the attention GEMMs (replicated on every rank)
+            ix = a + "indexer."
+            a_rows += [get(ix + "wk.weight"), get(ix + "weights_proj.weight")]
+            b_rows += [get(ix + "wq_b.weight")]
+        qkv_a = Linear(_quantize(torch.cat(a_rows, 0), fmt_d, dev))
+        q_b = Linear(_quantize(torch.cat(b_rows, 0), fmt_d, dev))
         kvb = split(get(a + "kv_b_proj.weight").view(H, cfg.qk_nope_head_dim + cfg.v_head_dim, -1), 0,
                     attn_tp, attn_rank)
         wdt = torch.bfloat16 if dev.type == "cuda" else torch.float32
@@ -90,11 +97,8 @@ def build_model(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState,
                          w_uk=w_uk, w_uv=w_uv, o_proj=Linear(_quantize(o, fmt_d, dev)))
         if cfg.index_n_heads:
             ix = a + "indexer."
-            aw.ix_wq_b = Linear(get(ix + "wq_b.weight").to(dev, wdt))
-            aw.ix_wk = get(ix + "wk.weight").to(dev, wdt)
             aw.ix_k_norm_w = sd[ix + "k_norm.weight"].float().to(dev)
             aw.ix_k_norm_b = sd[ix + "k_norm.bias"].float().to(dev)
-            aw.ix_weights = get(ix + "weights_proj.weight").to(dev, wdt)
         m = p + "mlp."
         if cfg.is_moe_layer(i):
             per = cfg.n_routed_experts // ps.ep_size

@@ -92,19 +92,18 @@ def build_random_model(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState, 
     # attention + dense + shared weights first (distinct per layer)
     attn_list, dense_list, shared_list = [], [], []
     for i in range(cfg.num_hidden_layers):
-        qkv_a = Linear(rand_mx((), cfg.q_lora_rank + cfg.kv_cache_dim, h, dev, sd))
-        q_b = Linear(rand_mx((), Hl * cfg.qk_head_dim, cfg.q_lora_rank, dev, sd))
+        ix_rows = cfg.index_head_dim + cfg.index_n_heads if cfg.index_n_heads else 0
+        ixq_rows = cfg.index_n_heads * cfg.index_head_dim if cfg.index_n_heads else 0
+        qkv_a = Linear(rand_mx((), cfg.q_lora_rank + cfg.kv_cache_dim + ix_rows, h, dev, sd))
+        q_b = Linear(rand_mx((), Hl * cfg.qk_head_dim + ixq_rows, cfg.q_lora_rank, dev, sd))
         o = Linear(rand_mx((), h, Hl * cfg.v_head_dim, dev, sd))
         w_uk = rand_bf16((Hl, cfg.qk_nope_head_dim, cfg.kv_lora_rank), dev, gen)
         w_uv = rand_bf16((Hl, cfg.v_head_dim, cfg.kv_lora_rank), dev, gen)
         aw = AttnWeights(qkv_a=qkv_a, q_a_ln=ones(cfg.q_lora_rank), kv_a_ln=ones(cfg.kv_lora_rank), q_b=q_b,
                          w_uk=w_uk, w_uv=w_uv, o_proj=o)
         if cfg.index_n_heads:
-            aw.ix_wq_b = Linear(rand_bf16((cfg.index_n_heads * cfg.index_head_dim, cfg.q_lora_rank), dev, gen))
-            aw.ix_wk = rand_bf16((cfg.index_head_dim, h), dev, gen)
             aw.ix_k_norm_w = ones(cfg.index_head_dim)
             aw.ix_k_norm_b = torch.zeros(cfg.index_head_dim, device=dev)
-            aw.ix_weights = rand_bf16((cfg.index_n_heads, h), dev, gen)
         attn_list.append(aw)
         if cfg.is_moe_layer(i):
             dense_list.append(None)

@@ -248,22 +248,42 @@ def mla_attention(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size, to
     return out.to(q_abs.dtype) if q_abs.is_cuda else out
 
 
-def index_k_store(k: torch.Tensor, cache: torch.Tensor, scale: torch.Tensor, slots: torch.Tensor) -> None:
-    """Indexer key cache: per-token e4m3 with an fp32 scale."""
+def index_k_store(k, ln_w, ln_b, eps: float, table, pos, cache: torch.Tensor, scale: torch.Tensor,
+                  slots: torch.Tensor) -> None:
+    """Indexer keys: LayerNorm -> RoPE on the first rope dims -> per-token
+    e4m3 (fp32 scale) into the paged indexer cache."""
+    if _use_native(k):
+        return _native().index_k_store(k, ln_w, ln_b, eps, table, pos, cache, scale, slots)
+    hd = k.shape[-1]
+    rd = table.shape[-1]
+    kf = torch.nn.functional.layer_norm(to_float(k), (hd,), ln_w.float(), ln_b.float(), eps)
+    kf = torch.cat([ref_rope(kf[:, :rd], pos, table), kf[:, rd:]], -1)
     if cache.dtype == torch.float8_e4m3fn:
-        amax = k.float().abs().amax(-1).clamp(min=1e-12)
-        s = amax / 448.0
-        cache[slots.long()] = (k.float() / s.unsqueeze(-1)).to(cache.dtype)
+        s = kf.abs().amax(-1).clamp(min=1e-12) / 448.0
+        cache[slots.long()] = (kf / s.unsqueeze(-1)).to(cache.dtype)
         scale[slots.long()] = s
     else:
-        cache[slots.long()] = k.to(cache.dtype)
+        cache[slots.long()] = kf.to(cache.dtype)
         scale[slots.long()] = 1.0
 
 
-def indexer_topk(q, w, k_cache, k_scale, fb, page_size, topk):
-    if _use_native(q):
-        return _native().indexer_topk(q, w, k_cache, k_scale, fb, page_size, topk)
+def indexer_topk(q_raw, w_raw, w_factor: float, table, k_cache, k_scale, fb, page_size: int, topk: int):
+    """Top-k cache positions [T, topk] (-1 padded, ascending) of the lightning
+    indexer: q_raw [T, NH*hd] before RoPE, w_raw [T, NH] head weights before
+    the w_factor scaling."""
+    if _use_native(q_raw):
+        return _native().indexer_topk(q_raw, w_raw, w_factor, table, k_cache, k_scale, fb, page_size, topk)
+    T, nh = w_raw.shape
+    rd = table.shape[-1]
+    q = to_float(q_raw).reshape(T, nh, -1)
+    q = torch.cat([ref_rope(q[..., :rd], fb.positions, table), q[..., rd:]], -1)
+    w = to_float(w_raw) * w_factor
     return ref.indexer_scores(q, w, k_cache, k_scale, fb.block_table, fb.q_seq, fb.positions, page_size, topk)
+
+
+def ref_rope(x: torch.Tensor, pos: torch.Tensor, table: torch.Tensor) -> torch.Tensor:
+    from ..models.rope import apply_rope_ref
+    return apply_rope_ref(x.float(), pos, table)
 
 
 # ---------------------------------------------------------------------------

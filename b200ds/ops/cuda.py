@@ -190,7 +190,7 @@ def mla_attention(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size, to
     out = torch.empty(T, H, L, dtype=torch.bfloat16, device=dev)
     qa = q_abs.to(torch.bfloat16).contiguous()
     qp = q_pe.to(torch.bfloat16).contiguous()
-    use_tc = (impl or "tc") == "tc" and topk is None and page_size == 64 and L == 512 and H % 16 == 0 \
+    use_tc = (impl or "tc") == "tc" and page_size == 64 and L == 512 and H % 16 == 0 \
         and q_pe.shape[-1] == 64
     if not use_tc:
         _C.mla_simt(qa, qp, cache.view(torch.uint8), kv_scale, fb.block_table, fb.q_seq, fb.positions, topk,
@@ -199,13 +199,17 @@ def mla_attention(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size, to
     q8 = torch.empty(T, H, 576, dtype=torch.uint8, device=dev)
     qs = torch.empty(T, H, dtype=torch.float32, device=dev)
     _C.mla_q_quant(qa, qp, q8, qs)
-    nsplit = mla_splits(T, H, int(fb.max_seq_len) if fb.max_seq_len else 4096) if fb.is_decode else 1
+    keys = int(fb.max_seq_len) if fb.max_seq_len else 4096
+    if topk is not None:
+        keys = min(keys, int(topk.shape[1]))
+        topk = topk.to(torch.int32).contiguous()
+    nsplit = mla_splits(T, H, keys) if (fb.is_decode or topk is not None) else 1
     po = pl = None
     if nsplit > 1:
         po = torch.empty(nsplit, T, H, L, dtype=torch.float32, device=dev)
         pl = torch.empty(nsplit, T, H, dtype=torch.float32, device=dev)
     _C.mla_tc(q8, qs, cache.view(torch.uint8), kv_scale, fb.block_table, fb.q_seq, fb.positions, page_size,
-              softmax_scale, nsplit, out, po, pl)
+              softmax_scale, nsplit, out, po, pl, topk)
     return out
 
 
@@ -284,9 +288,42 @@ def moe_experts(h, w: torch.Tensor, ids: torch.Tensor, ex, out_dtype=torch.bfloa
 
 
 # ---------------------------------------------------------------------------
-def indexer_topk(q, w, k_cache, k_scale, fb, page_size, topk):
-    from . import ref
-    return ref.indexer_scores(q, w, k_cache, k_scale, fb.block_table, fb.q_seq, fb.positions, page_size, topk)
+def index_k_store(k, ln_w, ln_b, eps, table, pos, cache, scale, slots):
+    _C.ix_k_store(k, ln_w, ln_b, eps, pos, table, slots, cache.view(torch.uint8), scale)
+
+
+def ix_splits(T: int, max_len: int) -> int:
+    """Key splits of the indexer score grid: cover ~2 waves of SMs, at least
+    two 128-key tiles per CTA."""
+    tiles = max(1, -(-max_len // 128))
+    return max(1, min(64, -(-296 // max(T, 1)), max(1, tiles // 2)))
+
+
+_IX_SCORE_BYTES = 512 << 20      # cap on the fp32 score scratch per call
+
+
+def indexer_topk(q_raw, w_raw, w_factor, table, k_cache, k_scale, fb, page_size, topk):
+    """Indexer: RoPE + e4m3 queries, tcgen05 scores, radix top-k.  Queries are
+    processed in slices so the [T, capacity] fp32 score scratch stays bounded."""
+    T, nh = w_raw.shape
+    dev = q_raw.device
+    cap = int(fb.block_table.shape[1]) * page_size
+    out = torch.empty(T, topk, dtype=torch.int32, device=dev)
+    kc = k_cache.view(torch.uint8)
+    step = max(1, min(T, _IX_SCORE_BYTES // (cap * 4)))
+    max_len = int(fb.max_seq_len) if fb.max_seq_len else cap
+    for t0 in range(0, T, step):
+        t1 = min(T, t0 + step)
+        n = t1 - t0
+        q8 = torch.empty(n * nh, 128, dtype=torch.uint8, device=dev)
+        wq = torch.empty(n, nh, dtype=torch.float32, device=dev)
+        pos = fb.positions[t0:t1]
+        _C.ix_q_quant(q_raw[t0:t1], w_raw[t0:t1], nh, w_factor, pos, table, q8, wq)
+        scores = torch.empty(n, cap, dtype=torch.float32, device=dev)
+        _C.ix_score(q8, wq, kc, k_scale, fb.block_table, fb.q_seq[t0:t1], pos, page_size,
+                    ix_splits(n, max_len), scores)
+        _C.topk_select(scores, pos, out[t0:t1])
+    return out
 
 
 def sample(logits, temperature, top_p, top_k, uniform):

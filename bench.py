@@ -85,11 +85,26 @@ def parse():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="native", choices=["native", "baseline", "reference"])
-    p.add_argument("--model", default="deepseek-v3-671b")
-    p.add_argument("--batch", type=int, default=64)
-    p.add_argument("--input-len", type=int, default=1024)
+    p.add_argument("--config", default="v3-1k", choices=sorted(BENCH_CONFIGS),
+                   help="named workload: v3-1k (headline: 671B, 64 x 1K), v32-sparse-32k (671B + lightning "
+                        "indexer top-2048, 8 x 32K)")
+    p.add_argument("--model", default=None)
+    p.add_argument("--batch", type=int, default=None)
+    p.add_argument("--input-len", type=int, default=None)
     p.add_argument("--weight-sets", type=int, default=0)
-    return p.parse_args()
+    a = p.parse_args()
+    d = BENCH_CONFIGS[a.config]
+    a.model = a.model or d["model"]
+    a.batch = a.batch or d["batch"]
+    a.input_len = a.input_len or d["input_len"]
+    return a
+
+
+# Named workloads (model preset, concurrent requests, input tokens each).
+BENCH_CONFIGS = {
+    "v3-1k": {"model": "deepseek-v3-671b", "batch": 64, "input_len": 1024},
+    "v32-sparse-32k": {"model": "deepseek-v3.2-sparse-671b", "batch": 8, "input_len": 32768},
+}
 
 
 def log(msg: str) -> None:
@@ -125,15 +140,18 @@ def main():
     if args.impl == "native":
         import b200ds._C  # noqa: F401
     cfg = PRESETS[args.model]()
+    ctx = args.input_len + args.warmup + 2 * args.steps + 8
     ecfg = EngineConfig(tp_size=world, ep_size=world, page_size=64, max_num_seqs=args.batch,
                         max_prefill_tokens=16384, cuda_graphs=True, graph_batch_sizes=(args.batch,),
-                        enable_prefix_cache=False, weight_sets=args.weight_sets)
+                        enable_prefix_cache=False, weight_sets=args.weight_sets,
+                        max_model_len=max(16384, ctx + 64))
     t0 = time.time()
     log(f"building {args.model} on {world} GPU(s)")
-    model = build_random_model(cfg, ecfg, ps, dev, seed=0)
+    kv_per_tok = cfg.num_hidden_layers * (cfg.kv_cache_dim + (cfg.index_head_dim + 4 if cfg.index_n_heads else 0))
+    reserve = 24e9 + args.batch * (ctx + 64) * kv_per_tok
+    model = build_random_model(cfg, ecfg, ps, dev, seed=0, reserve_bytes=reserve)
     torch.cuda.synchronize()
     t_init = time.time() - t0
-    ctx = args.input_len + args.warmup + 2 * args.steps + 8
     pages_per_seq = (ctx + ecfg.page_size - 1) // ecfg.page_size
     eng = Engine(model, ecfg, num_pages=args.batch * pages_per_seq + 8)
     eng.graphs.max_pages = pages_per_seq
@@ -239,7 +257,8 @@ def main():
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,
             "clocks": clocks,
-            "config": {"model": args.model, "global_batch": args.batch, "seq_len": args.input_len,
+            "config": {"name": args.config, "model": args.model, "global_batch": args.batch,
+                       "seq_len": args.input_len,
                        "context_during_timing": [args.input_len + args.warmup, args.input_len + args.warmup + 2 * args.steps],
                        "parallelism": f"tp{world}-attn+ep{world}-moe", "weight_sets": getattr(model, "weight_sets", None),
                        "l2": "no flush: per-step weights+KV >> 126 MB L2", "init_s": round(t_init, 1)},

@@ -25,7 +25,21 @@ struct MlaTcArgs {
   float* part_o;            // [nsplit, T, H, 512]
   float* part_lse;          // [nsplit, T, H]
   uint32_t* err;
+  const int* topk = nullptr;  // [T, topk_n] cache positions (-1 = none): sparse MLA
+  int topk_n = 0;
 };
+// Lightning indexer (sparse MLA): key store, query quantisation, tcgen05
+// scores and the top-k radix select.
+int b200_ix_k_store(const void* k, int f32, int64_t ld, int T, const float* ln_w, const float* ln_b, float eps,
+                    const int* pos, const float* table, int R, const int64_t* slots, uint8_t* cache, float* scale,
+                    cudaStream_t st);
+int b200_ix_q_quant(const void* q, int q_f32, int64_t ldq, const void* wraw, int w_f32, int64_t ldw, int T, int NH,
+                    float w_factor, const int* pos, const float* table, int R, uint8_t* q8, float* wq, cudaStream_t st);
+int b200_ix_score(const uint8_t* q8, const float* wq, int T, int NH, const uint8_t* k_cache, int64_t cache_rows,
+                  const float* k_scale, const int* block_table, int bt_stride, const int* q_seq, const int* q_pos,
+                  int page_size, int nsplit, float* scores, int64_t ld, uint32_t* err, cudaStream_t st);
+int b200_topk_select(const float* scores, int64_t ld, const int* q_pos, int T, int K, int* out, cudaStream_t st);
+
 int b200_mla_q_quant(const void* q_abs, const void* q_pe, int TH, uint8_t* q8, float* qs, cudaStream_t st);
 int b200_mla_tc(const MlaTcArgs* args, cudaStream_t st);
 

@@ -19,6 +19,14 @@
 // Warp roles (192 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA
 // issuer, warps 2-5 softmax / correction / epilogue.  All waits bounded.
 //
+// Sparse variant (SPARSE = true): the query attends only to the cache
+// positions in its top-k list (-1 = unused entry).  The KV rows of a tile are
+// then scattered over pages, so the whole producer warp gathers them with
+// 16-byte cp.async copies written in the same 128B / 64B swizzled layout the
+// TMA boxes would produce (the MMA descriptors are shared with the dense
+// path); a proxy fence makes the copies visible to the tensor cores before
+// the stage's barrier is signalled.
+//
 // Reference parity: the reference's own sparse-MLA decode kernel `bsx`
 // (ro_unit.cu:480; c36s SPA design ro_unit.cu:136-172) uses the same
 // transposed S^T / O^T arrangement with e4m3 P; this kernel is written from
@@ -78,11 +86,14 @@ struct Params {
   float* part_o;             // [nsplit, T, H, 512] when nsplit > 1
   float* part_lse;           // [nsplit, T, H]
   uint32_t* err;
+  const uint8_t* cache;      // e4m3 [rows, 576] (sparse gathers)
+  const int* topk;           // [T, topk_n] cache positions, -1 = none (sparse)
+  int topk_n;
 };
 
 __device__ __forceinline__ void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 
-template <int HB>
+template <int HB, bool SPARSE>
 __global__ void __launch_bounds__(kThreads, 1)
 mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constant__ CUtensorMap tm_q_rope,
               const __grid_constant__ CUtensorMap tm_kv_lat, const __grid_constant__ CUtensorMap tm_kv_rope,
@@ -116,15 +127,18 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
   pdl_launch_dependents();   // dependents wait for this grid before touching its outputs
   const int b = p.q_seq[t];
   const int n = p.q_pos[t] + 1;
-  // KV tokens per split adapt to this query's own length (graph-safe).
-  const int chunk = (((n + p.nsplit - 1) / p.nsplit) + kTile - 1) / kTile * kTile;
+  // Keys: cache positions [0, n) (dense) or the first min(topk_n, n) entries
+  // of the query's top-k list (sparse).  Keys per split adapt to this
+  // query's own length (graph-safe).
+  const int nk = SPARSE ? min(p.topk_n, n) : n;
+  const int chunk = (((nk + p.nsplit - 1) / p.nsplit) + kTile - 1) / kTile * kTile;
   const int k_lo = split * chunk;
-  const int k_hi = min(n, k_lo + chunk);
+  const int k_hi = min(nk, k_lo + chunk);
   const int nt = k_hi > k_lo ? (k_hi - k_lo + kTile - 1) / kTile : 0;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_full[i], SPARSE ? 32 : 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 1);
@@ -145,7 +159,43 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
 
   if (warp == 0) {
     // ------------------------------ producer ------------------------------
-    if (lane == 0 && nt > 0) {
+    if (SPARSE && nt > 0) {
+      if (lane == 0) {
+        const int qrow = t * p.H + h0;
+        mbar_arrive_expect_tx(q_full, S::kQLat + S::kQRope);
+        for (int c = 0; c < 4; ++c) tma_load_2d(sQ + c * HB * 128, &tm_q_lat, q_full, c * 128, qrow);
+        tma_load_2d(sQ + S::kQLat, &tm_q_rope, q_full, kL, qrow);
+      }
+      __syncwarp();
+      const int* list = p.topk + (int64_t)t * p.topk_n;
+      for (int i = 0; i < nt; ++i) {
+        const int s = i % kStages;
+        if (i >= kStages && !mbar_wait(&kv_empty[s], ((i / kStages) - 1) & 1, p.err)) break;
+        const uint32_t dst = smem_u32(sKV + s * S::kKVStage);
+        const int tok0 = k_lo + i * kTile;
+#pragma unroll 1
+        for (int q = 0; q < kTile / 32; ++q) {
+          const int r = q * 32 + lane;                       // row of the tile
+          const int j = tok0 + r;                            // list entry
+          const int pos = j < k_hi ? __ldg(list + j) : -1;
+          const bool ok = pos >= 0 && pos < n;
+          int64_t slot = 0;
+          if (ok) slot = (int64_t)__ldg(p.block_table + (int64_t)b * p.bt_stride + pos / kPage) * kPage + pos % kPage;
+          const uint8_t* src = p.cache + slot * kD;
+          const uint32_t nb = ok ? 16u : 0u;
+#pragma unroll
+          for (int c = 0; c < 32; ++c)                       // latent: 4 boxes of 128 B, 128B swizzle
+            cp_async_16(dst + (c >> 3) * kTile * 128 + r * 128 + (((c & 7) ^ (r & 7)) << 4), src + c * 16, nb);
+#pragma unroll
+          for (int c = 0; c < 4; ++c)                        // rope: 64 B rows, 64B swizzle
+            cp_async_16(dst + S::kKVLat + r * 64 + ((c ^ ((r >> 1) & 3)) << 4), src + kL + c * 16, nb);
+        }
+        cp_async_commit();
+        cp_async_wait_all();
+        fence_proxy_async_smem();
+        mbar_arrive(&kv_full[s]);
+      }
+    } else if (!SPARSE && lane == 0 && nt > 0) {
       const int qrow = t * p.H + h0;
       mbar_arrive_expect_tx(q_full, S::kQLat + S::kQRope);
       for (int c = 0; c < 4; ++c) tma_load_2d(sQ + c * HB * 128, &tm_q_lat, q_full, c * 128, qrow);
@@ -243,7 +293,11 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
           uint32_t r[16];
           tmem_ld_x16(base + c0, r);
           tmem_ld_wait();
-          const bool valid = tok0 + row < k_hi;
+          bool valid = tok0 + row < k_hi;
+          if (SPARSE && valid) {
+            const int pos = __ldg(p.topk + (int64_t)t * p.topk_n + tok0 + row);
+            valid = pos >= 0 && pos < n;
+          }
 #pragma unroll
           for (int j = 0; j < 16; ++j)
             sS[row * (HB + 1) + c0 + j] = valid ? __uint_as_float(r[j]) * sHead[c0 + j] : -INFINITY;
@@ -447,7 +501,7 @@ static int map2d(CUtensorMap* m, const void* base, int64_t rows, int box_rows, i
   return r == CUDA_SUCCESS ? 0 : int(r);
 }
 
-template <int HB>
+template <int HB, bool SPARSE>
 static int launch(const MlaTcArgs& a, cudaStream_t st) {
   using S = Smem<HB>;
   CUtensorMap mql, mqr, mkl, mkr;
@@ -471,7 +525,10 @@ static int launch(const MlaTcArgs& a, cudaStream_t st) {
   p.part_o = a.part_o;
   p.part_lse = a.part_lse;
   p.err = a.err;
-  auto kern = mla_tc_kernel<HB>;
+  p.cache = a.cache;
+  p.topk = a.topk;
+  p.topk_n = a.topk_n;
+  auto kern = mla_tc_kernel<HB, SPARSE>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes);
   dim3 grid(a.T, a.H / HB, a.nsplit);
   b200::launch_pdl(kern, dim3(grid), dim3(kThreads), S::kBytes, st, mql, mqr, mkl, mkr, p);
@@ -498,9 +555,16 @@ int b200_mla_tc(const MlaTcArgs* a, cudaStream_t st) {
   using namespace b200::mla;
   if (a->T <= 0) return 0;
   if (a->page_size != kPage || a->nsplit < 1 || a->nsplit > 16) return -1;
-  if (a->H % 64 == 0) return launch<64>(*a, st);
-  if (a->H % 32 == 0) return launch<32>(*a, st);
-  if (a->H % 16 == 0) return launch<16>(*a, st);
+  if (a->topk != nullptr) {
+    if (a->topk_n <= 0) return -1;
+    if (a->H % 64 == 0) return launch<64, true>(*a, st);
+    if (a->H % 32 == 0) return launch<32, true>(*a, st);
+    if (a->H % 16 == 0) return launch<16, true>(*a, st);
+    return -6;
+  }
+  if (a->H % 64 == 0) return launch<64, false>(*a, st);
+  if (a->H % 32 == 0) return launch<32, false>(*a, st);
+  if (a->H % 16 == 0) return launch<16, false>(*a, st);
   return -6;
 }
 

@@ -318,6 +318,14 @@ B200_DEVICE void bulk_load_hint(void* smem_dst, const void* gsrc, uint32_t bytes
       ::"r"(smem_u32(smem_dst)), "l"(gsrc), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
+// 16-byte cp.async (L2-only) with zero fill: src_bytes 0 writes 16 zero bytes.
+// Used for row gathers whose rows are too scattered for a tiled TMA box.
+B200_DEVICE void cp_async_16(uint32_t smem_dst, const void* gsrc, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_dst), "l"(gsrc), "r"(src_bytes) : "memory");
+}
+B200_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+B200_DEVICE void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 B200_DEVICE void named_barrier(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 }  // namespace b200
 

@@ -264,3 +264,119 @@ def test_moe_experts_skewed_routing(T, hot):
     exc = ExpertWeights(0, E, MXFP8Tensor(ex.w13.data.cpu(), ex.w13.sf.cpu()), MXFP8Tensor(ex.w2.data.cpu(), ex.w2.sf.cpu()), I)
     exp = ops.moe_experts(dequant_mxfp8(a.data, a.sf).cpu(), wts.cpu(), ids.cpu(), exc, torch.float32)
     assert rel_err(got.cpu(), exp) < 3e-2, rel_err(got.cpu(), exp)
+
+
+# ---------------------------------------------------------------------------
+# Sparse MLA: lightning indexer + top-k + tcgen05 sparse attention
+# ---------------------------------------------------------------------------
+
+def _paged(lens, ps=64, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    pages_per = [(n + ps - 1) // ps for n in lens]
+    bt = torch.zeros(len(lens), max(pages_per) + 1, dtype=torch.int32)
+    perm = torch.randperm(sum(pages_per), generator=g) + 1
+    k = 0
+    for b in range(len(lens)):
+        for j in range(pages_per[b]):
+            bt[b, j] = int(perm[k])
+            k += 1
+    return bt, (sum(pages_per) + 1) * ps
+
+
+def test_ix_k_store_matches_reference():
+    from b200ds import ops
+    from b200ds.config import v32_sparse_config
+    from b200ds.models.rope import cos_sin_table
+    cfg = v32_sparse_config()
+    table = cos_sin_table(cfg, 4096)
+    T, slots = 37, 512
+    k = (torch.randn(T, 128) * 2).to(torch.bfloat16)
+    ln_w, ln_b = torch.rand(128) + 0.5, torch.randn(128) * 0.1
+    pos = torch.randint(0, 4000, (T,), dtype=torch.int32)
+    sl = torch.randperm(slots)[:T].to(torch.int64)
+    c_ref = torch.zeros(slots, 128, dtype=torch.float8_e4m3fn)
+    s_ref = torch.ones(slots)
+    ops.index_k_store(k.float(), ln_w, ln_b, 1e-6, table, pos, c_ref, s_ref, sl)   # CPU tensors: reference
+    c = torch.zeros(slots, 128, dtype=torch.float8_e4m3fn, device=DEV)
+    s = torch.ones(slots, device=DEV)
+    ops.index_k_store(k.to(DEV), ln_w.to(DEV), ln_b.to(DEV), 1e-6, table.to(DEV), pos.to(DEV), c, s, sl.to(DEV))
+    got = c.cpu().float() * s.cpu().unsqueeze(-1)
+    exp = c_ref.float() * s_ref.unsqueeze(-1)
+    assert rel_err(got[sl], exp[sl]) < 2e-2
+    assert torch.allclose(s.cpu()[sl], s_ref[sl], rtol=1e-3)
+
+
+@pytest.mark.parametrize("lens,decode", [([300, 1, 2100, 64], True), ([700, 129], False), ([33000], True)])
+def test_ix_score_and_topk(lens, decode):
+    """tcgen05 indexer scores vs fp32 math on the same e4m3 operands; radix
+    top-k vs torch.topk on those scores."""
+    from types import SimpleNamespace
+    from b200ds.ops import cuda
+    from b200ds.config import v32_sparse_config
+    from b200ds.models.rope import cos_sin_table
+    torch.manual_seed(1)
+    cfg = v32_sparse_config()
+    table = cos_sin_table(cfg, 40000).to(DEV)
+    NH, K = 64, 2048
+    bt, rows = _paged(lens)
+    kc = (torch.randn(rows, 128) * 0.5).to(torch.float8_e4m3fn)
+    ks = torch.rand(rows) + 0.5
+    if decode:
+        q_seq = torch.arange(len(lens), dtype=torch.int32)
+        q_pos = torch.tensor([n - 1 for n in lens], dtype=torch.int32)
+    else:
+        q_seq = torch.tensor([b for b in range(len(lens)) for _ in range(3)], dtype=torch.int32)
+        q_pos = torch.tensor([max(0, n - 3 + j) for n in lens for j in range(3)], dtype=torch.int32)
+    T = q_seq.numel()
+    q_raw = (torch.randn(T, NH * 128) * 0.3).to(torch.bfloat16).to(DEV)
+    w_raw = torch.randn(T, NH).to(torch.bfloat16).to(DEV)
+    fb = SimpleNamespace(block_table=bt.to(DEV), q_seq=q_seq.to(DEV), positions=q_pos.to(DEV),
+                         is_decode=decode, max_seq_len=max(lens))
+    from b200ds import _C
+    q8 = torch.empty(T * NH, 128, dtype=torch.uint8, device=DEV)
+    wq = torch.empty(T, NH, device=DEV)
+    _C.ix_q_quant(q_raw, w_raw, NH, 0.01, fb.positions, table, q8, wq)
+    cap = bt.shape[1] * 64
+    scores = torch.full((T, cap), float("nan"), device=DEV)
+    _C.ix_score(q8, wq, kc.view(torch.uint8).to(DEV), ks.to(DEV), fb.block_table, fb.q_seq, fb.positions, 64,
+                cuda.ix_splits(T, max(lens)), scores)
+    out = torch.empty(T, K, dtype=torch.int32, device=DEV)
+    _C.topk_select(scores, fb.positions, out)
+    q8f = q8.view(torch.float8_e4m3fn).float().cpu().view(T, NH, 128)
+    sc, out = scores.cpu(), out.cpu()
+    for t in range(T):
+        b, n = int(q_seq[t]), int(q_pos[t]) + 1
+        pos = torch.arange(n)
+        slots = bt[b, pos // 64].long() * 64 + pos % 64
+        kf = kc[slots].float()
+        exp = ((q8f[t] @ kf.T).relu() * wq[t].cpu().unsqueeze(-1)).sum(0) * ks[slots]
+        assert rel_err(sc[t, :n], exp) < 1e-4
+        kk = min(K, n)
+        want = sorted(sc[t, :n].topk(kk).indices.tolist())
+        got = out[t, :kk].tolist()
+        assert got == want
+        assert (out[t, kk:] == -1).all()
+
+
+@pytest.mark.parametrize("H,lens", [(16, [3000, 40, 2100]), (128, [5000]), (32, [2048, 2049])])
+def test_mla_tc_sparse_matches_reference(H, lens):
+    from types import SimpleNamespace
+    from b200ds.ops import cuda, ref
+    torch.manual_seed(2)
+    L, R, K = 512, 64, 2048
+    bt, rows = _paged(lens)
+    cache = (torch.randn(rows, L + R) * 0.5).to(torch.float8_e4m3fn)
+    B = len(lens)
+    q_seq = torch.arange(B, dtype=torch.int32)
+    q_pos = torch.tensor([n - 1 for n in lens], dtype=torch.int32)
+    topk = torch.full((B, K), -1, dtype=torch.int32)
+    for b, n in enumerate(lens):
+        kk = min(K, n)
+        topk[b, :kk] = torch.randperm(n)[:kk].sort().values.to(torch.int32)
+    q_abs = (torch.randn(B, H, L) * 0.3).to(torch.bfloat16)
+    q_pe = (torch.randn(B, H, R) * 0.3).to(torch.bfloat16)
+    fb = SimpleNamespace(block_table=bt.to(DEV), q_seq=q_seq.to(DEV), positions=q_pos.to(DEV),
+                         is_decode=True, max_seq_len=max(lens))
+    got = cuda.mla_attention(q_abs.to(DEV), q_pe.to(DEV), cache.to(DEV), 0.7, fb, 0.0625, 64, topk.to(DEV))
+    exp = ref.mla_attention(q_abs, q_pe, cache, 0.7, bt, torch.tensor(lens), q_seq, q_pos, 0.0625, 64, topk)
+    assert rel_err(got.cpu(), exp) < 3e-2
