@@ -68,7 +68,7 @@ class DecodeGraphRunner:
         g.h_tok = torch.zeros(bs, dtype=torch.int64).pin_memory()
         g.fb = ForwardBatch(input_ids=g.ids, positions=g.pos, q_seq=g.q_seq, out_slots=g.slots, seq_lens=g.lens,
                             block_table=g.bt, last_idx=g.last, is_decode=True, max_q_len=1,
-                            max_seq_len=self.max_pages * self.page_size)
+                            max_seq_len=self.max_pages * self.page_size, dp_tmax=bs)
         return g
 
     def capture(self, bs: int) -> _Graph:
@@ -124,12 +124,16 @@ class DecodeGraphRunner:
         g.lens.copy_(g.h_lens, non_blocking=True)
         g.bt.copy_(g.h_bt, non_blocking=True)
 
-    def run(self, step, seqs: List[dict]) -> List[int]:
+    def run(self, step, seqs: List[dict], bucket: Optional[int] = None) -> Optional[List[int]]:
+        """Replay the graph of `bucket` (default: the smallest that fits);
+        `step` None replays with padding rows only (an idle DP rank)."""
         n = len(seqs)
-        bs = self._bucket(n)
+        bs = bucket or self._bucket(n)
         g = self.graphs.get(bs) or self.capture(bs)
         self.stage(g, seqs)
         g.graph.replay()
+        if step is None:
+            return None
         greedy = all(r.params.temperature <= 0 for r in step.reqs)
         if greedy:
             g.h_tok.copy_(g.tokens, non_blocking=True)

@@ -3,7 +3,8 @@
 Every rank of an SPMD job (torchrun, one process per GPU) constructs the
 Engine and calls `generate` with the same requests; schedules, page tables
 and sampled tokens are identical on every rank, so no host broadcast is
-needed between steps.  The server (b200ds.server) drives rank 0 and
+needed between steps.  Under DP attention (EngineConfig.dp_attention) each
+rank instead serves its own requests and the ranks step in lockstep.  The server (b200ds.server) drives rank 0 and
 forwards requests to the other ranks over the gloo control group.
 
 Per step: the scheduler picks a prefill or decode batch; the host builds the
@@ -67,6 +68,10 @@ class Engine:
             from .cuda_graph import DecodeGraphRunner
             self.graphs = DecodeGraphRunner(self)
         self.stats: Dict[str, float] = {"steps": 0, "prefill_tokens": 0, "decode_tokens": 0}
+        # DP attention: every rank schedules its own requests; ranks agree
+        # each step on the mode and on the per-rank token rows of the MoE
+        # exchange (gloo, host only), and an idle rank joins with a dummy.
+        self.dp = bool(ecfg.dp_attention) and self.ps.ep_size > 1
 
     def _auto_pages(self) -> int:
         if self.device.type != "cuda":
@@ -95,6 +100,34 @@ class Engine:
         logits = self.model.forward(fb)
         return self._sample(step, logits)
 
+    def _dp_forward(self, step: Optional[Step]) -> Optional[List[int]]:
+        """One lockstep DP-attention forward.  All ranks run the same kind of
+        forward: the decode graph of the largest rank's bucket when every
+        rank decodes, else eager with dp_tmax = the largest rank's tokens.
+        Returns None when no rank has work, [] for an idle rank that joined
+        with a dummy forward, else this rank's sampled tokens."""
+        import torch.distributed as dist
+        ntok = 0 if step is None else sum(len(c) for c in step.chunks)
+        nseq = 0 if step is None else len(step.reqs)
+        prefill = step is not None and step.kind == "prefill"
+        v = torch.tensor([int(prefill), ntok, nseq, int(step is not None)], dtype=torch.int64)
+        dist.all_reduce(v, op=dist.ReduceOp.MAX, group=self.ps.cpu_group)
+        any_prefill, max_tok, max_seq, any_work = (int(x) for x in v)
+        if not any_work:
+            return None
+        seqs = [] if step is None else [{"tokens": ch, "start": st, "pages": r.pages}
+                                        for r, ch, st in zip(step.reqs, step.chunks, step.starts)]
+        if not any_prefill and self.graphs is not None and self.graphs.can_run(max_seq):
+            toks = self.graphs.run(step, seqs, bucket=self.graphs._bucket(max_seq))
+            return [] if toks is None else toks
+        if step is None:      # idle rank: one dummy token on the scratch page
+            seqs = [{"tokens": [0], "start": 0, "pages": [0]}]
+        fb = build_batch(seqs, self.ecfg.page_size, device="cpu")
+        fb.dp_tmax = max(max_tok, 1)
+        fb = self._to_device(fb)
+        logits = self.model.forward(fb)
+        return [] if step is None else self._sample(step, logits)
+
     def _to_device(self, fb: ForwardBatch) -> ForwardBatch:
         if self.device.type == "cpu":
             return fb
@@ -121,9 +154,14 @@ class Engine:
     def step(self) -> List[Request]:
         """Run one scheduler step; returns requests that finished."""
         st = self.sched.next_step()
-        if st is None:
+        if self.dp:
+            toks = self._dp_forward(st)
+            if st is None:
+                return []
+        elif st is None:
             return []
-        toks = self._forward(st)
+        else:
+            toks = self._forward(st)
         self.sched.commit(st)
         now = time.perf_counter()
         done = []
@@ -160,6 +198,10 @@ class Engine:
         reqs = [self.add_request(p, sp) for p, sp in zip(prompts, params)]
         while any(not r.finished for r in reqs):
             self.step()
+        if self.dp:
+            # keep stepping (as an idle rank) until every rank is done
+            while self._dp_forward(None) is not None:
+                pass
         outs = []
         for r in reqs:
             n = len(r.output)

@@ -25,6 +25,9 @@ class ForwardBatch:
     is_decode: bool = False
     max_q_len: int = 1
     max_seq_len: int = 0
+    # DP attention: token rows per rank this step (the max over ranks), which
+    # sizes the expert-parallel exchange; 0 = this batch's own token count.
+    dp_tmax: int = 0
     # Optional per-request sampling parameters (engine fills them)
     temperature: Optional[torch.Tensor] = None
     top_p: Optional[torch.Tensor] = None

@@ -115,10 +115,22 @@ class DeepseekModel:
         self.ix_cache: List[torch.Tensor] = []
         self.ix_scale: List[torch.Tensor] = []
         self.page_size = ecfg.page_size
+        # DP attention: each rank serves its own requests with replicated
+        # attention / dense / shared-expert / LM-head weights (tp_size 1);
+        # only the routed experts are split (EP) and exchanged at the MoE
+        # boundary.  ps_local is the single-rank view for local reductions.
+        self.dp = bool(ecfg.dp_attention) and ps.ep_size > 1
+        self.ps_local = ParallelState(device=self.device) if self.dp else ps
         if (self.device.type == "cuda" and ps.tp_size > 1 and ecfg.comm_impl == "fused"
                 and getattr(ps, "fused_ar", None) is None):
             from ..parallel.symm import FusedAllReduce
             ps.fused_ar = FusedAllReduce(ps, cfg.hidden_size, max_tokens=max(ecfg.max_num_seqs, 256))
+        if (self.device.type == "cuda" and self.dp and ecfg.comm_impl == "fused" and cfg.n_routed_experts
+                and getattr(ps, "fused_ep", None) is None):
+            from ..parallel.symm import EPDispatch, FusedAllReduce
+            cap = max(ecfg.max_num_seqs, 256)
+            ps.fused_ar = FusedAllReduce(ps, cfg.hidden_size, max_tokens=cap, group="ep")
+            ps.fused_ep = EPDispatch(ps, cfg.hidden_size, cfg.num_experts_per_tok, cap)
 
     # ------------------------------------------------------------------
     def allocate_kv(self, num_pages: int):
@@ -161,7 +173,7 @@ class DeepseekModel:
         o_lat = ops.mla_attention(q_abs, q_pe, self.kv_cache[i], self.kv_scale[i], fb,
                                   c.softmax_scale, self.page_size, topk)
         o = ops.absorb_o(o_lat, aw.w_uv)                                  # [T, Hl*v]
-        if self.device.type == "cuda" and self.ps.tp_size > 1:
+        if self.device.type == "cuda" and self.attn_tp > 1:
             # leave the o_proj GEMM to the all-reduce so it can run fused
             return ops.PendingLinear(o, aw.o_proj.w, aw.o_proj.out_features)
         return aw.o_proj(o, out_dtype=torch.float32 if self.device.type == "cpu" else torch.bfloat16)
@@ -190,6 +202,8 @@ class DeepseekModel:
                 return ops.PendingLinear(a, lw.ffn.down.w, lw.ffn.down.out_features)
             return lw.ffn.down(a, out_dtype=out_dt)
         mw: MoEWeights = lw.ffn
+        if self.dp:
+            return self._moe_dp(mw, h, fb)
         w, ids = ops.router(h, mw.gate, mw.bias, c)
         if fuse and ops.get_impl() == "native":
             # The shared expert is independent of the routed experts: run it on
@@ -209,6 +223,42 @@ class DeepseekModel:
             s = lw.ffn.shared_down(ops.gate_up_swiglu(h, mw.shared_gate_up), out_dtype=out_dt)
             out = out + s
         return out
+
+    def _moe_dp(self, mw: MoEWeights, h, fb: ForwardBatch):
+        """MoE under DP attention: this rank's T_r tokens (padded to the
+        step's agreed T_step rows per rank) meet the routed experts of every
+        rank.  Fused path: router on the local tokens, P2P dispatch to the
+        expert owners, grouped GEMMs over the received tokens, and the
+        combine + reduce-scatter fused into the next norm.  Host-collective
+        path (CPU, baseline ops, steps larger than the symmetric buffers):
+        all-gather, local experts over all tokens, all-reduce, own slice."""
+        c, ps = self.cfg, self.ps
+        T_r = fb.num_tokens
+        T_step = max(int(fb.dp_tmax or 0), T_r)
+        out_dt = torch.float32 if self.device.type == "cpu" else torch.bfloat16
+        ep, far = getattr(ps, "fused_ep", None), getattr(ps, "fused_ar", None)
+        if (self.device.type == "cuda" and ops.get_impl() == "native" and ep is not None and ep.supports(T_step)
+                and far is not None and far.supports(T_step)):
+            shared = None
+            if mw.shared_gate_up is not None:
+                shared = self._fork(lambda: mw.shared_down(ops.gate_up_swiglu(h, mw.shared_gate_up),
+                                                           out_dtype=out_dt), h)
+            w, ids = ops.router(h, mw.gate, mw.bias, c)
+            part = ops.moe_experts_ep(h, w, ids, mw.experts, T_step, c.n_routed_experts, ep)
+            if shared is not None:
+                part.add = self._join(shared)
+            return part
+        x = ops.to_float(h)
+        if T_step > T_r:
+            x = torch.cat([x, x.new_zeros(T_step - T_r, x.shape[1])], 0)
+        g = ps.ep_all_gather(x.to(out_dt).contiguous())
+        w, ids = ops.router(g, mw.gate, mw.bias, c)
+        part = ops.moe_experts(g, w, ids, mw.experts, out_dtype=torch.float32, n_experts_total=c.n_routed_experts)
+        ps.ep_all_reduce(part)
+        out = part[ps.ep_rank * T_step: ps.ep_rank * T_step + T_r]
+        if mw.shared_gate_up is not None:
+            out = out + mw.shared_down(ops.gate_up_swiglu(h, mw.shared_gate_up), out_dtype=torch.float32).float()
+        return out.to(out_dt)
 
     # ------------------------------------------------------------------
     def _fork(self, fn, *inputs):
@@ -245,8 +295,11 @@ class DeepseekModel:
                                                     self.ps, "tp_attn", self._ffn_first_linear(lw))
             f = self._ffn(i, lw, h, fb)
             nxt = self.layers[i + 1] if i + 1 < len(self.layers) else None
+            # under DP attention only the fused expert-parallel partial still
+            # needs a collective; every other FFN output is already this rank's
+            ps_f = self.ps if (not self.dp or isinstance(f, ops.EPPartial)) else self.ps_local
             h, residual = ops.allreduce_add_rmsnorm(
-                f, residual, nxt.in_ln if nxt else self.final_ln, c.rms_norm_eps, self.ps,
+                f, residual, nxt.in_ln if nxt else self.final_ln, c.rms_norm_eps, ps_f,
                 "ffn", nxt.attn.qkv_a if nxt else None)
         last = ops.to_float(h)[fb.last_idx] if not isinstance(h, torch.Tensor) or h.dim() == 2 else h[fb.last_idx]
         return ops.lm_head_logits(last, self.lm_head, self.ps)

@@ -88,6 +88,20 @@ class MoEPartial:
     add: Optional[torch.Tensor] = None
 
 
+@dataclass
+class EPPartial:
+    """Expert-parallel MoE output before its combine + reduce-scatter: weighted
+    expert rows y over the world * T_step received tokens, their (token, k)
+    row index pair_row [world * T_step, K], this rank's T_r own tokens and an
+    optional additive partial for them (shared expert).  Consumed by the
+    fused reduce-scatter + residual + RMSNorm."""
+    y: torch.Tensor
+    pair_row: torch.Tensor
+    T_step: int
+    T_r: int
+    add: Optional[torch.Tensor] = None
+
+
 def materialize(a, out_dtype=torch.bfloat16) -> torch.Tensor:
     if isinstance(a, PendingLinear):
         y = linear(a.x, a.w, out_dtype)
@@ -152,7 +166,7 @@ def allreduce_add_rmsnorm(a: torch.Tensor, residual: torch.Tensor, w: torch.Tens
     Returns (normalized activation, new residual).  ``a`` may be a
     PendingLinear / MoEPartial, which the fused path folds into its GEMM or
     combine kernel."""
-    if residual.is_cuda and ps.tp_size > 1 and _IMPL == "native":
+    if residual.is_cuda and _IMPL == "native" and (ps.tp_size > 1 or isinstance(a, EPPartial)):
         return _native().allreduce_add_rmsnorm(a, residual, w, eps, ps, next_linear)
     a = materialize(a, torch.float32 if not residual.is_cuda else torch.bfloat16)
     if ps.tp_size > 1 or (kind == "ffn" and ps.ep_size > 1):
@@ -297,6 +311,14 @@ def router(h, gate: torch.Tensor, bias: torch.Tensor, cfg):
     logits = x.float() @ gate.float().T
     return ref.router_topk(logits, bias, cfg.num_experts_per_tok, cfg.n_group, cfg.topk_group,
                            cfg.routed_scaling_factor, cfg.norm_topk_prob)
+
+
+def moe_experts_ep(h, w: torch.Tensor, ids: torch.Tensor, ex: ExpertWeights, T_step: int, n_experts_total: int,
+                   ep) -> EPPartial:
+    """Expert-parallel MoE on the fused NVLink path: dispatch this rank's
+    routed tokens to the expert owners, run the grouped GEMMs over the
+    received tokens; returns the partial for the fused combine."""
+    return _native().moe_experts_ep(h, w, ids, ex, T_step, n_experts_total, ep)
 
 
 def moe_experts(h, w: torch.Tensor, ids: torch.Tensor, ex: ExpertWeights, out_dtype=torch.float32,

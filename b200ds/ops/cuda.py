@@ -86,9 +86,14 @@ def allreduce_add_rmsnorm(a, residual, w, eps, ps, next_linear=None):
     """TP all-reduce + residual add + RMSNorm (+ MXFP8 quant): one fused
     NVLink kernel pair when the symmetric workspace is set up and the step
     fits it, else NCCL followed by the fused add+norm kernel."""
-    from . import MoEPartial, PendingLinear, materialize
+    from . import EPPartial, MoEPartial, PendingLinear, materialize
     far = getattr(ps, "fused_ar", None)
     T = residual.shape[0]
+    if isinstance(a, EPPartial):
+        quantized = next_linear is not None and getattr(next_linear, "quantized", False)
+        if residual.dtype != torch.float32:
+            residual = residual.float()
+        return far.ep_rs_add_rmsnorm(a, residual, w, eps, quantized)
     if far is not None and far.supports(T):
         quantized = next_linear is not None and getattr(next_linear, "quantized", False)
         if residual.dtype != torch.float32:
@@ -285,6 +290,48 @@ def moe_experts(h, w: torch.Tensor, ids: torch.Tensor, ex, out_dtype=torch.bfloa
     out = torch.empty(T, Hd, dtype=out_dtype, device=dev)
     _C.moe_combine(y, pair_row, None, out)
     return out
+
+
+def moe_experts_ep(h, w, ids, ex, T_step: int, n_experts_total: int, ep):
+    """Expert-parallel MoE: ep_dispatch (P2P push of routed rows) -> ep_align
+    (bounded wait + routing layout over all ranks' tokens) -> ep_gather ->
+    persistent FC1 (SwiGLU + requant) -> FC2 (routing-weighted); the combine
+    + reduce-scatter runs fused in the following norm step."""
+    from . import EPPartial, QAct
+    a = h if isinstance(h, QAct) else quant(h)
+    T_r, Hd = a.q.shape
+    K = ids.shape[1]
+    E = ex.count
+    dev = a.q.device
+    I = ex.inter
+    Tg = ep.world * T_step
+    exp_rows = Tg * K / n_experts_total
+    bn1 = moe_tile_n(exp_rows, 64)
+    bn2 = moe_tile_n(exp_rows, 128)
+    max_rows = round_up(Tg * K, 128) + E * 128
+    ids = (ids if ids.dtype == torch.int32 else ids.int()).contiguous()
+    _C.ep_dispatch(a.q, a.sf, ids, w.float().contiguous(), T_step, n_experts_total // ep.world, ep.bases, ep.rank,
+                   ep.max_t, ep.epoch, ep.push_ticket)
+    seg_start = torch.empty(E, dtype=torch.int32, device=dev)
+    seg_count = torch.empty(E, dtype=torch.int32, device=dev)
+    tt1 = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    tt2 = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    row_token = torch.empty(max_rows, dtype=torch.int32, device=dev)
+    row_weight = torch.empty(max_rows, dtype=torch.float32, device=dev)
+    pair_row = torch.empty(Tg, K, dtype=torch.int32, device=dev)
+    total = torch.empty(1, dtype=torch.int32, device=dev)
+    _C.ep_align(ep.bases, ep.rank, ep.max_t, Hd, K, T_step, ex.first, E, seg_start, seg_count, row_token, row_weight,
+                pair_row, total, bn1, tt1, bn2, tt2, ep.epoch, ep.err)
+    xs = alloc_qact(max_rows, Hd, dev)
+    _C.ep_gather(ep.bases, ep.rank, ep.max_t, Hd, K, T_step, pair_row, xs.q, xs.sf, ep.epoch, ep.gather_ticket)
+    hq = alloc_qact(max_rows, I, dev)
+    w13, w2 = ex.w13, ex.w2
+    _C.gemm_grouped(w13.data, w13.sf, xs.q, xs.sf, 2 * I, Hd, E, I, bn1, seg_start, seg_count, tt1, 2,
+                    None, 0, hq.q, hq.sf, I, None, 0, True)
+    y = torch.empty(max_rows, Hd, dtype=torch.bfloat16, device=dev)
+    _C.gemm_grouped(w2.data, w2.sf, hq.q, hq.sf, Hd, I, E, 0, bn2, seg_start, seg_count, tt2, 3,
+                    y, Hd, None, None, 0, row_weight, 0, True)
+    return EPPartial(y, pair_row, T_step, T_r)
 
 
 # ---------------------------------------------------------------------------

@@ -44,6 +44,7 @@ class ParallelState:
     cpu_group: Optional[object] = None
     device: torch.device = torch.device("cpu")
     fused_ar: Optional[object] = None       # parallel.symm.FusedAllReduce when enabled
+    fused_ep: Optional[object] = None       # parallel.symm.EPDispatch (DP attention + EP)
 
     @property
     def distributed(self) -> bool:
@@ -59,6 +60,14 @@ class ParallelState:
         if self.ep_size > 1:
             dist.all_reduce(x, group=self.ep_group)
         return x
+
+    def ep_all_gather(self, x: torch.Tensor) -> torch.Tensor:
+        """[T, ...] per rank -> [ep_size * T, ...] in rank order."""
+        if self.ep_size == 1:
+            return x
+        parts = [torch.empty_like(x) for _ in range(self.ep_size)]
+        dist.all_gather(parts, x.contiguous(), group=self.ep_group)
+        return torch.cat(parts, 0)
 
     def tp_all_gather(self, x: torch.Tensor, dim: int = -1) -> torch.Tensor:
         if self.tp_size == 1:

@@ -19,17 +19,18 @@ import torch.distributed as dist
 
 
 class FusedAllReduce:
-    def __init__(self, ps, hidden: int, max_tokens: int = 256, push_ctas: int = 296):
+    def __init__(self, ps, hidden: int, max_tokens: int = 256, push_ctas: int = 296, group: str = "tp"):
         import torch.distributed._symmetric_memory as symm_mem
         from .. import _C
         self.ps = ps
         self.hidden = hidden
         self.max_tokens = max_tokens
         self.push_ctas = push_ctas
-        self.world = ps.tp_size
-        self.rank = ps.tp_rank
+        if group == "ep":       # expert-parallel reduce-scatter under DP attention
+            self.world, self.rank, group = ps.ep_size, ps.ep_rank, ps.ep_group
+        else:
+            self.world, self.rank, group = ps.tp_size, ps.tp_rank, ps.tp_group
         dev = ps.device
-        group = ps.tp_group
         name = group.group_name
         if hasattr(symm_mem, "enable_symm_mem_for_group") and not symm_mem.is_symm_mem_enabled_for_group(name):
             symm_mem.enable_symm_mem_for_group(name)
@@ -110,8 +111,59 @@ class FusedAllReduce:
         y, qa = self._outs(T, H, part.y.device, quantize)
         return self._reduce(T, H, 1, residual, ln_w, eps, y, qa)
 
+    def ep_rs_add_rmsnorm(self, part, residual, ln_w, eps, quantize):
+        """Expert-parallel combine: each received token's partial goes to its
+        owner's slot (reduce-scatter), then this rank's reduce + residual +
+        norm over its own T_r tokens."""
+        from .. import _C
+        H = part.y.shape[1]
+        add = part.add.to(torch.bfloat16).contiguous() if part.add is not None else None
+        _C.ep_combine_rs(part.y, part.pair_row, part.T_step, part.T_r, add, self.bases, self.rank, self.max_tokens,
+                         self.epoch, self.push_ticket, self.push_ctas)
+        y, qa = self._outs(part.T_r, H, part.y.device, quantize)
+        return self._reduce(part.T_r, H, 1, residual, ln_w, eps, y, qa)
+
     def check(self) -> None:
         """Raise if a bounded wait inside the kernels timed out."""
         e = int(self.err.item())
         if e:
             raise RuntimeError(f"fused all-reduce: peer wait timed out (code {e})")
+
+
+class EPDispatch:
+    """Symmetric dispatch buffer of the expert-parallel MoE (DP attention):
+    two parities of [world * max_tokens] received MXFP8 token rows plus their
+    routing rows, arrival counters, and the device epoch / tickets of the
+    dispatch -> align -> gather protocol (csrc/comm/ep.cu)."""
+
+    def __init__(self, ps, hidden: int, topk: int, max_tokens: int):
+        import torch.distributed._symmetric_memory as symm_mem
+        from .. import _C
+        self.world = ps.ep_size
+        self.rank = ps.ep_rank
+        self.max_t = max_tokens
+        self.hidden = hidden
+        dev = ps.device
+        group = ps.ep_group
+        name = group.group_name
+        if hasattr(symm_mem, "enable_symm_mem_for_group") and not symm_mem.is_symm_mem_enabled_for_group(name):
+            symm_mem.enable_symm_mem_for_group(name)
+        nbytes = int(_C.ep_buffer_size(self.world, max_tokens, hidden, topk))
+        self.buf = symm_mem.empty(nbytes, dtype=torch.uint8, device=dev)
+        self.buf.zero_()
+        self.hdl = symm_mem.rendezvous(self.buf, name)
+        self.bases = [int(p) for p in self.hdl.buffer_ptrs]
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.push_ticket = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.gather_ticket = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=group)
+
+    def supports(self, T_step: int) -> bool:
+        return 0 < T_step <= self.max_t
+
+    def check(self) -> None:
+        e = int(self.err.item())
+        if e:
+            raise RuntimeError(f"expert-parallel dispatch: peer wait timed out (code {e})")

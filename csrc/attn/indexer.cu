@@ -328,9 +328,18 @@ topk_select_kernel(const float* scores, int64_t ld, const int* q_pos, int K, int
     const int shift = 8 * d;
     for (int i = tid; i < 256; i += kTopkThreads) hist[i] = 0;
     __syncthreads();
-    for (int i = tid; i < n; i += kTopkThreads) {
-      const uint32_t u = order_key(sc[i]);
-      if ((u & mask) == prefix) atomicAdd(&hist[(u >> shift) & 255], 1);
+    // Scores of one query crowd into a few exponent bins, so lanes that hit
+    // the same bin combine their increments (one shared atomic per bin per
+    // warp instead of one per lane).
+    for (int i0 = 0; i0 < n; i0 += kTopkThreads) {
+      const int i = i0 + tid;
+      int bin = -1;
+      if (i < n) {
+        const uint32_t u = order_key(sc[i]);
+        if ((u & mask) == prefix) bin = (u >> shift) & 255;
+      }
+      const unsigned peers = __match_any_sync(0xffffffffu, bin);
+      if (bin >= 0 && (threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&hist[bin], __popc(peers));
     }
     __syncthreads();
     if (tid < 32) {

@@ -28,7 +28,7 @@
 // EPA epilogue push (epa.py:795, epa_gemm.py:1849-1890); here every poll is
 // bounded and reports an error code instead of hanging.
 #include "../common/ptx.cuh"
-#include "comm.h"
+#include "comm_dev.cuh"
 
 namespace b200 {
 namespace comm {
@@ -36,48 +36,15 @@ namespace comm {
 constexpr int kThreads = 256;
 constexpr int kMaxIt = 8;     // hidden <= 256 * 8 * 8 = 16384
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void red_release_sys_add(uint32_t* p, uint32_t v) {
-  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
 __device__ __forceinline__ int64_t sf_off(int row, int kblock, int kb_total) {
   const int rb = row >> 7, r = row & 127, kc = kblock >> 2, c = kblock & 3;
   return ((int64_t)(rb * (kb_total >> 2) + kc) << 9) + ((r & 31) << 4) + ((r >> 5) << 2) + c;
 }
 
-// Called by every CTA of a push grid after its peer stores: each CTA fences
-// and takes a local ticket; the last one publishes once per rank (one
-// system-scope increment per destination instead of one per CTA, which
-// serialised thousands of atomics on the same counter word).
 __device__ __forceinline__ void publish_push(const ArPeers& peers, int parity, uint32_t* ticket) {
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    const uint32_t prev = atomicAdd(ticket, 1u);
-    if (prev == gridDim.x * gridDim.y * gridDim.z - 1) {
-      __threadfence_system();
-      *ticket = 0u;
-      for (int q = 0; q < peers.world; ++q)
-        asm volatile("red.release.sys.global.add.u32 [%0], %1;"
-                     ::"l"(reinterpret_cast<uint32_t*>(peers.base[q]) + parity * kArMaxRanks + peers.rank), "r"(1u)
-                     : "memory");
-    }
-  }
+  publish_push(peers.base, peers.world, peers.rank, parity, ticket);
 }
 
-__device__ __forceinline__ uint32_t* counters(uint8_t* base, int parity) {
-  return reinterpret_cast<uint32_t*>(base) + parity * kArMaxRanks;
-}
-__device__ __forceinline__ __nv_bfloat16* recv_slot(uint8_t* base, int parity, int src, int world, int max_t,
-                                                    int hidden) {
-  return reinterpret_cast<__nv_bfloat16*>(base + kArRecvOff) +
-         ((int64_t)(parity * world + src) * max_t) * hidden;
-}
 
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads) ar_push_kernel(const __nv_bfloat16* __restrict__ x, int T, int hidden,

@@ -67,6 +67,83 @@ void moe_combine_push(const at::Tensor& y, const at::Tensor& pair_row, c10::opti
 
 int64_t ar_buffer_size(int64_t world, int64_t max_t, int64_t hidden) { return ar_buffer_bytes(world, max_t, hidden); }
 
+// ---------------------------------------------------------------------------
+// Expert-parallel dispatch / combine
+EpPeers make_ep(const std::vector<int64_t>& bases, int64_t rank, int64_t max_t, int64_t hidden, int64_t K) {
+  TORCH_CHECK(bases.size() >= 1 && bases.size() <= (size_t)kArMaxRanks, "1..8 ranks");
+  EpPeers p{};
+  for (size_t i = 0; i < bases.size(); ++i) p.base[i] = reinterpret_cast<uint8_t*>(bases[i]);
+  p.rank = rank;
+  p.world = bases.size();
+  p.max_t = max_t;
+  p.hidden = hidden;
+  p.K = K;
+  ep_layout(p.world, max_t, hidden, K, &p.par_bytes, &p.off_sf, &p.off_ids, &p.off_w);
+  return p;
+}
+
+int64_t ep_buffer_size(int64_t world, int64_t max_t, int64_t hidden, int64_t K) {
+  return ep_buffer_bytes(world, max_t, hidden, K);
+}
+
+cudaStream_t cur() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void ep_dispatch(const at::Tensor& q, const at::Tensor& sf, const at::Tensor& ids, const at::Tensor& w, int64_t T_step,
+                 int64_t experts_per_rank, std::vector<int64_t> bases, int64_t rank, int64_t max_t, const at::Tensor& epoch,
+                 at::Tensor ticket) {
+  TORCH_CHECK(q.is_cuda() && q.dim() == 2 && q.is_contiguous(), "q e4m3 [T, hidden]");
+  TORCH_CHECK(ids.scalar_type() == at::kInt && ids.is_contiguous() && w.scalar_type() == at::kFloat && w.is_contiguous(),
+              "ids int32 / w fp32 [T, K]");
+  const c10::cuda::CUDAGuard g(q.device());
+  EpPeers p = make_ep(bases, rank, max_t, q.size(1), ids.size(1));
+  const int rc = b200_ep_dispatch(reinterpret_cast<const uint8_t*>(q.data_ptr()),
+                                  reinterpret_cast<const uint8_t*>(sf.data_ptr()), ids.data_ptr<int>(),
+                                  w.data_ptr<float>(), ids.size(0), T_step, experts_per_rank, &p,
+                                  reinterpret_cast<const uint32_t*>(epoch.data_ptr()),
+                                  reinterpret_cast<uint32_t*>(ticket.data_ptr()), cur());
+  TORCH_CHECK(rc == 0, "ep_dispatch failed ", rc);
+}
+
+void ep_align(std::vector<int64_t> bases, int64_t rank, int64_t max_t, int64_t hidden, int64_t K, int64_t T_step,
+              int64_t first, int64_t E, at::Tensor seg_start, at::Tensor seg_count, at::Tensor row_token,
+              at::Tensor row_weight, at::Tensor pair_row, at::Tensor total_rows, int64_t bn1, at::Tensor ttile1,
+              int64_t bn2, at::Tensor ttile2, const at::Tensor& epoch, at::Tensor err) {
+  const c10::cuda::CUDAGuard g(pair_row.device());
+  EpPeers p = make_ep(bases, rank, max_t, hidden, K);
+  TORCH_CHECK(pair_row.numel() == p.world * T_step * K, "pair_row [world*T_step, K]");
+  const int rc = b200_ep_align(&p, T_step, first, E, seg_start.data_ptr<int>(), seg_count.data_ptr<int>(),
+                               row_token.data_ptr<int>(), row_weight.data_ptr<float>(), pair_row.data_ptr<int>(),
+                               total_rows.data_ptr<int>(), bn1, ttile1.data_ptr<int>(), bn2, ttile2.data_ptr<int>(),
+                               reinterpret_cast<const uint32_t*>(epoch.data_ptr()),
+                               reinterpret_cast<uint32_t*>(err.data_ptr()), cur());
+  TORCH_CHECK(rc == 0, "ep_align failed ", rc);
+}
+
+void ep_gather(std::vector<int64_t> bases, int64_t rank, int64_t max_t, int64_t hidden, int64_t K, int64_t T_step,
+               const at::Tensor& pair_row, at::Tensor dq, at::Tensor dsf, at::Tensor epoch, at::Tensor ticket) {
+  const c10::cuda::CUDAGuard g(pair_row.device());
+  EpPeers p = make_ep(bases, rank, max_t, hidden, K);
+  const int rc = b200_ep_gather(&p, T_step, pair_row.data_ptr<int>(), reinterpret_cast<uint8_t*>(dq.data_ptr()),
+                                reinterpret_cast<uint8_t*>(dsf.data_ptr()), reinterpret_cast<uint32_t*>(epoch.data_ptr()),
+                                reinterpret_cast<uint32_t*>(ticket.data_ptr()), cur());
+  TORCH_CHECK(rc == 0, "ep_gather failed ", rc);
+}
+
+void ep_combine_rs(const at::Tensor& y, const at::Tensor& pair_row, int64_t T_step, int64_t T_r,
+                   c10::optional<at::Tensor> add, std::vector<int64_t> bases, int64_t rank, int64_t max_t,
+                   const at::Tensor& epoch, at::Tensor ticket, int64_t nctas) {
+  TORCH_CHECK(y.is_cuda() && y.scalar_type() == at::kBFloat16 && y.is_contiguous(), "y bf16");
+  TORCH_CHECK(pair_row.scalar_type() == at::kInt && pair_row.is_contiguous(), "pair_row int32");
+  if (add.has_value() && add->defined())
+    TORCH_CHECK(add->scalar_type() == at::kBFloat16 && add->is_contiguous(), "add bf16 [T_r, hidden]");
+  const c10::cuda::CUDAGuard g(y.device());
+  ArPeers p = make_peers(bases, rank, max_t);
+  const int rc = b200_ep_combine_rs(y.data_ptr(), pair_row.data_ptr<int>(), T_step, T_r, pair_row.size(1), y.size(1),
+                                    optr<void>(add), &p, reinterpret_cast<const uint32_t*>(epoch.data_ptr()),
+                                    reinterpret_cast<uint32_t*>(ticket.data_ptr()), nctas, cur());
+  TORCH_CHECK(rc == 0, "ep_combine_rs failed ", rc);
+}
+
 }  // namespace
 
 void register_comm(pybind11::module& m) {
@@ -74,4 +151,9 @@ void register_comm(pybind11::module& m) {
   m.def("ar_reduce_norm", &ar_reduce_norm);
   m.def("ar_buffer_size", &ar_buffer_size);
   m.def("moe_combine_push", &moe_combine_push);
+  m.def("ep_buffer_size", &ep_buffer_size);
+  m.def("ep_dispatch", &ep_dispatch);
+  m.def("ep_align", &ep_align);
+  m.def("ep_gather", &ep_gather);
+  m.def("ep_combine_rs", &ep_combine_rs);
 }

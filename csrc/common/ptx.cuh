@@ -6,6 +6,7 @@
 // %globaltimer deadline, record an error code in a device word the host
 // checks, and return, so a protocol bug cannot hang a shared GPU.
 #pragma once
+#include <cstdlib>
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -356,6 +357,16 @@ namespace b200 {
 // the previous kernel in the stream drains; every kernel of this project
 // executes griddepcontrol.wait before it reads its predecessor's outputs or
 // writes anything, and triggers its own dependents at entry.
+// B200_NO_PDL=1 in the environment launches plainly instead (a diagnostic:
+// per-kernel profiles then show each kernel's own duration rather than one
+// stretched by an early start).
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("B200_NO_PDL");
+    return !(e && e[0] == '1');
+  }();
+  return on;
+}
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
                               Args&&... args) {
@@ -368,7 +379,7 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 }  // namespace b200

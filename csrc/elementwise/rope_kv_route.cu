@@ -7,6 +7,7 @@
 // record it writes for the expert GEMMs (rr.py:1-15).
 #include "../common/ptx.cuh"
 #include "elementwise.h"
+#include "moe_layout.cuh"
 
 namespace b200 {
 namespace ew2 {
@@ -183,54 +184,11 @@ __global__ void moe_align_kernel(const int* ids, const float* w, int T, int K, i
                                  int* seg_count, int* row_token, float* row_weight, int* pair_row, int* total_rows,
                                  int bn1, int* ttile1, int bn2, int* ttile2) {
   extern __shared__ int sh[];
-  int* cnt = sh;          // [E]
-  int* start = sh + E;    // [E]
-  int* fill = sh + 2 * E; // [E]
   pdl_wait();
   pdl_launch_dependents();   // dependents wait for this grid before touching its outputs
-  for (int e = threadIdx.x; e < E; e += blockDim.x) { cnt[e] = 0; fill[e] = 0; }
-  __syncthreads();
-  const int n = T * K;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const int e = ids[i] - first;
-    if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int acc = 0, a1 = 0, a2 = 0;
-    for (int e = 0; e < E; ++e) {
-      start[e] = acc;
-      acc += (cnt[e] + 127) & ~127;
-      if (ttile1) ttile1[e] = a1;
-      if (ttile2) ttile2[e] = a2;
-      a1 += (cnt[e] + bn1 - 1) / bn1;
-      a2 += (cnt[e] + bn2 - 1) / bn2;
-    }
-    if (ttile1) ttile1[E] = a1;
-    if (ttile2) ttile2[E] = a2;
-    *total_rows = acc;
-  }
-  __syncthreads();
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    seg_start[e] = start[e];
-    seg_count[e] = cnt[e];
-  }
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const int e = ids[i] - first;
-    if (e >= 0 && e < E) {
-      const int r = start[e] + atomicAdd(&fill[e], 1);
-      row_token[r] = i / K;
-      row_weight[r] = w[i];
-      pair_row[i] = r;
-    } else {
-      pair_row[i] = -1;
-    }
-  }
+  moe::moe_align_body(ids, w, T, K, first, E, seg_start, seg_count, row_token, row_weight, pair_row, total_rows, bn1,
+                      ttile1, bn2, ttile2, sh);
 }
-
-// Gather MXFP8 rows for the local experts: for routed pair i = (t, j) with a
-// local expert, sorted row pair_row[i] <- token row t (data + scale bytes).
-// grid (T*K), block 128.
 __global__ void moe_gather_kernel(const uint8_t* xq, const uint8_t* xsf, const int* pair_row, int npairs, int K,
                                   int Kd, uint8_t* dq, uint8_t* dsf) {
   const int i = blockIdx.x;
@@ -239,19 +197,9 @@ __global__ void moe_gather_kernel(const uint8_t* xq, const uint8_t* xsf, const i
   if (i >= npairs) return;
   const int r = pair_row[i];
   if (r < 0) return;
-  const int t = i / K;
-  const uint4* s = reinterpret_cast<const uint4*>(xq + (int64_t)t * Kd);
-  uint4* d = reinterpret_cast<uint4*>(dq + (int64_t)r * Kd);
-  for (int i = threadIdx.x; i < Kd / 16; i += blockDim.x) d[i] = s[i];
-  const int kb = Kd / 32;
-  for (int b = threadIdx.x; b < kb; b += blockDim.x) {
-    const int64_t so = ((int64_t)((t >> 7) * (kb >> 2) + (b >> 2)) << 9) + ((t & 31) << 4) + (((t & 127) >> 5) << 2) + (b & 3);
-    const int64_t doff = ((int64_t)((r >> 7) * (kb >> 2) + (b >> 2)) << 9) + ((r & 31) << 4) + (((r & 127) >> 5) << 2) + (b & 3);
-    dsf[doff] = xsf[so];
-  }
+  moe::moe_gather_pair(xq, xsf, i / K, r, Kd, dq, dsf);
 }
 
-// out[t, :] = sum_j y[pair_row[t*K+j], :] (+ add[t, :]) in fp32 -> bf16 / f32.
 __global__ void moe_combine_kernel(const __nv_bfloat16* y, const int* pair_row, int T, int K, int D, const void* add,
                                    int add_f32, void* out, int out_f32) {
   const int t = blockIdx.x;

@@ -362,7 +362,7 @@ static int launch(const GroupedArgs& a, cudaStream_t st) {
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = a.pdl ? 1 : 0;
+  attr[0].val.programmaticStreamSerializationAllowed = (a.pdl && b200::pdl_enabled()) ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, ma, mb, p) == cudaSuccess ? 0 : 1;

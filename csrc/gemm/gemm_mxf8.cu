@@ -512,7 +512,7 @@ static int launch_t(const GemmArgs& a, cudaStream_t st) {
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = a.pdl ? 1 : 0;
+  attr[0].val.programmaticStreamSerializationAllowed = (a.pdl && b200::pdl_enabled()) ? 1 : 0;
   int nattr = 1;
   if (C::kCluster) {
     attr[1].id = cudaLaunchAttributeClusterDimension;

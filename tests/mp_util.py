@@ -43,13 +43,17 @@ def run_ranks(fn, world: int, *args, timeout: float = 300.0):
             if p.is_alive():
                 p.kill()
                 raise TimeoutError("rank did not finish")
-        out = []
+        out, errs = [], []
         for r in range(world):
             f = os.path.join(d, f"r{r}.pt")
             if not os.path.exists(f):
-                raise RuntimeError(f"rank {r} produced no result (exit {procs[r].exitcode})")
+                errs.append(f"rank {r} produced no result (exit {procs[r].exitcode})")
+                continue
             o = torch.load(f, weights_only=False)
             if not o["ok"]:
-                raise RuntimeError(f"rank {r} failed:\n{o['err']}")
+                errs.append(f"rank {r} failed:\n{o['err']}")
+                continue
             out.append(o["res"])
+        if errs:
+            raise RuntimeError("\n".join(errs))
         return out

@@ -1,0 +1,60 @@
+"""DP attention + EP MoE on CPU (gloo, 2 ranks): each rank serves its own
+requests, the MoE exchanges tokens between ranks, and every request's tokens
+and prefill logits must match a single-process run of all requests."""
+import torch
+
+from mp_util import run_ranks
+
+
+def _prompts(cfg):
+    g = torch.Generator().manual_seed(7)
+    # uneven: rank 0 serves 2 requests, rank 1 one shorter request, so the
+    # ranks' token counts differ and rank 1 idles (dummy forwards) at the end
+    lens = [20, 13, 9]
+    return [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in lens]
+
+
+def _max_tokens():
+    return [10, 6, 14]
+
+
+def _run(cfg, ecfg, prompts, maxt, ps=None):
+    from b200ds import build_model_from
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.reference import init_weights
+    m = build_model_from(cfg, ecfg, init_weights(cfg, 0), device="cpu", ps=ps)
+    logs = []
+    orig = m.forward
+    m.forward = lambda fb: logs.append((fb.num_tokens, orig(fb))) or logs[-1][1]
+    eng = Engine(m, ecfg)
+    outs = eng.generate(prompts, [SamplingParams(max_tokens=n) for n in maxt])
+    return [o.token_ids for o in outs], logs
+
+
+def _rank(rank, world):
+    from b200ds.config import EngineConfig, tiny_config
+    from b200ds.parallel.state import init_parallel
+    ps = init_parallel(backend="gloo", dp_attention=True)
+    assert ps.tp_size == 1 and ps.ep_size == world
+    cfg = tiny_config()
+    ecfg = EngineConfig(page_size=8, cuda_graphs=False, tp_size=1, ep_size=world, dp_attention=True)
+    mine = [i for i in range(3) if i % world == rank]
+    prompts = [_prompts(cfg)[i] for i in mine]
+    maxt = [_max_tokens()[i] for i in mine]
+    toks, logs = _run(cfg, ecfg, prompts, maxt, ps)
+    return mine, toks, logs[0][1]
+
+
+def test_dp2_ep2_matches_single():
+    from b200ds.config import EngineConfig, tiny_config
+    cfg = tiny_config()
+    ref_toks, _ = _run(cfg, EngineConfig(page_size=8, cuda_graphs=False), _prompts(cfg), _max_tokens())
+    # single-process prefill logits of each prompt alone (the DP ranks'
+    # first forward is their own prompts' prefill)
+    res = run_ranks(_rank, 2)
+    for mine, toks, first_logits in res:
+        assert toks == [ref_toks[i] for i in mine]
+        _, logs = _run(cfg, EngineConfig(page_size=8, cuda_graphs=False), [_prompts(cfg)[i] for i in mine],
+                       [1] * len(mine))
+        assert (first_logits - logs[0][1]).abs().max() < 1e-4

@@ -98,3 +98,54 @@ def test_tp2_ep2_matches_single_gpu(comm_impl, kind, tol):
     assert e_tp2 <= 1.3 * e_tp1 + 0.01, (e_tp2, e_tp1)
     # ... and the two GPU runs differ by fp8 requantization noise only
     assert _rel(out0, ref) < 2.5 * tol, _rel(out0, ref)
+
+
+def _dp_batch(rank, cfg, dev):
+    from b200ds.models.batch import build_batch
+    g = torch.Generator().manual_seed(11 + rank)
+    if rank == 0:
+        toks = torch.randint(0, cfg.vocab_size, (12,), generator=g).tolist()
+        seqs = [{"tokens": toks[:5], "start": 0, "pages": [1]}, {"tokens": toks[5:], "start": 0, "pages": [2]}]
+    else:
+        toks = torch.randint(0, cfg.vocab_size, (9,), generator=g).tolist()
+        seqs = [{"tokens": toks, "start": 0, "pages": [3]}]
+    return build_batch(seqs, 64, device=dev)
+
+
+def _dp_rank(rank, world, comm_impl):
+    import torch
+    from b200ds import ops
+    from b200ds.config import EngineConfig, small_gpu_config
+    from b200ds.models.loader import build_model
+    from b200ds.models.reference import init_weights
+    from b200ds.parallel.state import ParallelState, init_parallel
+    ps = init_parallel(backend="nccl", dp_attention=True, timeout_s=60)
+    ops.set_impl("native")
+    cfg = small_gpu_config(num_attention_heads=16)
+    sd = init_weights(cfg, 0)
+    ecfg = EngineConfig(tp_size=1, ep_size=world, dp_attention=True, comm_impl=comm_impl)
+    m = build_model(cfg, ecfg, ps, sd, device=ps.device)
+    m.allocate_kv(8)
+    fb = _dp_batch(rank, cfg, ps.device)
+    fb.dp_tmax = 12                      # the larger rank's token rows
+    out = m.forward(fb).float().cpu()
+    single = build_model(cfg, EngineConfig(), ParallelState(device=ps.device), sd, device=ps.device)
+    single.allocate_kv(8)
+    ref = single.forward(_dp_batch(rank, cfg, ps.device)).float().cpu()
+    torch.cuda.synchronize()
+    for obj in (ps.fused_ar, ps.fused_ep):
+        if obj is not None:
+            obj.check()
+    return rank, out, ref
+
+
+@pytest.mark.parametrize("comm_impl", ["nccl", "fused"])
+def test_dp2_ep2_matches_single_gpu(comm_impl):
+    """DP attention + EP MoE on 2 GPUs, ranks with different token counts:
+    each rank's logits follow a 1-GPU run of its own batch (fp8 noise only).
+    The fused path exercises ep_dispatch / ep_align / ep_gather and the
+    combine + reduce-scatter into ar_reduce_norm."""
+    _needs(2)
+    res = run_ranks(_dp_rank, 2, comm_impl, timeout=600)
+    for rank, out, ref in res:
+        assert _rel(out, ref) < 0.15, (rank, _rel(out, ref))
