@@ -16,7 +16,7 @@ import torch
 
 from ..config import EngineConfig, ModelConfig
 from ..ops import ExpertWeights
-from ..ops.quant import MXFP8Tensor, mxfp8_from_block128, quant_mxfp8_ref, pack_sf, sf_packed_size
+from ..ops.quant import MXFP8Tensor, mxfp8_from_block128, quant_mxfp8_ref, pack_sf, sf_packed_size, NVFP4Tensor, quant_nvfp4_ref
 from ..parallel.state import ParallelState
 from .deepseek import AttnWeights, DeepseekModel, DenseWeights, LayerWeights, Linear, MoEWeights
 
@@ -37,12 +37,18 @@ def _quantize(w: torch.Tensor, fmt: str, device) -> object:
             return MXFP8Tensor(a.q, a.sf, rows)
         q, sf = quant_mxfp8_ref(wd.float())
         return MXFP8Tensor(q, sf, rows)
+    if fmt == "nvfp4":
+        t = quant_nvfp4_ref(w.to(device).float())
+        return t
     raise ValueError(f"unknown weight format {fmt}")
 
 
 def _stack(ws: List[object]) -> object:
     if isinstance(ws[0], MXFP8Tensor):
         return MXFP8Tensor(torch.stack([w.data for w in ws]), torch.stack([w.sf for w in ws]))
+    if isinstance(ws[0], NVFP4Tensor):
+        return NVFP4Tensor(torch.stack([w.data for w in ws]), torch.stack([w.sf for w in ws]),
+                           torch.stack([w.global_scale.reshape(()) for w in ws]), ws[0].rows)
     return torch.stack(ws)
 
 

@@ -22,7 +22,7 @@ import torch
 
 from ..config import EngineConfig, ModelConfig
 from ..ops import ExpertWeights
-from ..ops.quant import MXFP8Tensor, round_up
+from ..ops.quant import MXFP8Tensor, NVFP4Tensor, round_up
 from ..parallel.state import ParallelState
 from .deepseek import AttnWeights, DeepseekModel, DenseWeights, LayerWeights, Linear, MoEWeights
 
@@ -53,6 +53,23 @@ def rand_mx(shape_lead, N: int, K: int, dev, seeder: _Seeder) -> MXFP8Tensor:
     return MXFP8Tensor(data.view(torch.float8_e4m3fn), sf, N)
 
 
+# NVFP4 random weights: uniform random e2m1 codes (all 16 are finite, RMS
+# 2.93), unit e4m3 block scales (0x38 = 1.0) and a per-expert global scale
+# giving RMS ~0.018 like the MXFP8 weights.
+NVFP4_SCALE_BYTE = 0x38
+NVFP4_GLOBAL = 0.018 / 2.93
+
+
+def rand_nvfp4(E: int, N: int, K: int, dev, seeder: _Seeder) -> NVFP4Tensor:
+    from .. import _C
+    Np = round_up(N, 128)
+    data = torch.empty(E, Np, K // 2, dtype=torch.uint8, device=dev)
+    _C.fill_bytes(data, seeder.next(), 0xFF, 0)
+    sf = torch.full((E, Np * K // 16), NVFP4_SCALE_BYTE, dtype=torch.uint8, device=dev)
+    g = torch.full((E,), NVFP4_GLOBAL, dtype=torch.float32, device=dev)
+    return NVFP4Tensor(data, sf, g, N)
+
+
 def rand_bf16(shape, dev, gen, std=0.02, dtype=torch.bfloat16):
     t = torch.empty(shape, dtype=dtype, device=dev)
     t.normal_(0.0, std, generator=gen)
@@ -62,6 +79,8 @@ def rand_bf16(shape, dev, gen, std=0.02, dtype=torch.bfloat16):
 def expert_bytes_per_layer(cfg: ModelConfig, ep: int) -> int:
     per = cfg.n_routed_experts // ep
     h, I = cfg.hidden_size, cfg.moe_intermediate_size
+    if cfg.expert_format == "nvfp4":
+        return per * (2 * I * h + h * I) * (0.5 + 1 / 16)
     return per * (2 * I * h + h * I) * (1 + 1 / 32)
 
 
@@ -128,9 +147,14 @@ def build_random_model(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState, 
         reserve_bytes = 24e9 + kv_tokens * cfg.kv_cache_dim * cfg.num_hidden_layers
     sets = ecfg.weight_sets if ecfg.weight_sets > 0 else auto_weight_sets(cfg, ps, reserve_bytes, dev)
     expert_sets = []
+    fp4 = cfg.expert_format == "nvfp4"
     for s in range(min(sets, n_moe)):
-        w13 = rand_mx((per,), 2 * I, h, dev, sd)
-        w2 = rand_mx((per,), h, I, dev, sd)
+        if fp4:
+            w13 = rand_nvfp4(per, 2 * I, h, dev, sd)
+            w2 = rand_nvfp4(per, h, I, dev, sd)
+        else:
+            w13 = rand_mx((per,), 2 * I, h, dev, sd)
+            w2 = rand_mx((per,), h, I, dev, sd)
         expert_sets.append(ExpertWeights(first=first, count=per, w13=w13, w2=w2, inter=I))
     moe_idx = 0
     for i in range(cfg.num_hidden_layers):

@@ -17,7 +17,7 @@ import torch
 import torch.nn.functional as F
 
 from . import ref
-from .quant import MXFP8Tensor, quant_mxfp8_ref, dequant_mxfp8
+from .quant import MXFP8Tensor, quant_mxfp8_ref, dequant_mxfp8, NVFP4Tensor
 
 _IMPL = "native"
 
@@ -67,6 +67,9 @@ class ExpertWeights:
     w13: object
     w2: object
     inter: int
+    # NVFP4 experts: fixed fp32 global scale of the FC2 input (the SwiGLU
+    # output), so e4m3 block scales cover block maxima up to 448*6*scale.
+    fc2_act_scale: float = 1.0 / 32
 
 
 @dataclass
@@ -325,6 +328,11 @@ def moe_experts(h, w: torch.Tensor, ids: torch.Tensor, ex: ExpertWeights, out_dt
                 n_experts_total=None, combine: bool = True):
     """Local-expert part of the MoE: sum_k w[t,k] * expert_{ids[t,k]}(h[t]) over
     the experts this rank owns (others contribute on their ranks)."""
+    if isinstance(ex.w13, NVFP4Tensor):
+        x = h.hf if isinstance(h, QAct) and h.hf is not None else h
+        if (x.q if isinstance(x, QAct) else x).is_cuda and _IMPL == "native":
+            return _native().moe_experts_nvfp4(h, w, ids, ex, out_dtype, n_experts_total, combine)
+        return _moe_nvfp4_ref(to_float(h), w, ids, ex).to(out_dtype)
     if isinstance(ex.w13, MXFP8Tensor) and (h.q if isinstance(h, QAct) else h).is_cuda:
         if _IMPL == "native":
             return _native().moe_experts(h, w, ids, ex, out_dtype, n_experts_total, combine)
@@ -353,6 +361,29 @@ def moe_experts(h, w: torch.Tensor, ids: torch.Tensor, ex: ExpertWeights, out_dt
             o = y @ ex.w2[e].float().T
         out.index_add_(0, tok, we * o)
     return out.to(out_dtype)
+
+
+def _moe_nvfp4_ref(xf: torch.Tensor, w: torch.Tensor, ids: torch.Tensor, ex: ExpertWeights) -> torch.Tensor:
+    """fp32 reference of the NVFP4 experts, with the activations quantized as
+    the kernels do (FC1 input: per-token global scale; FC2 input: the fixed
+    fc2_act_scale)."""
+    from .quant import dequant_nvfp4_rows, quant_nvfp4_rows
+    T = xf.shape[0]
+    out = torch.zeros(T, xf.shape[1], dtype=torch.float32, device=xf.device)
+    for e in range(ex.count):
+        gid = ex.first + e
+        hit = (ids == gid)
+        tok = hit.any(-1).nonzero().flatten()
+        if tok.numel() == 0:
+            continue
+        we = (w.float() * hit).sum(-1)[tok].unsqueeze(-1)
+        a = dequant_nvfp4_rows(*quant_nvfp4_rows(xf[tok]))
+        w13 = dequant_nvfp4_rows(ex.w13.data[e], ex.w13.sf[e], ex.w13.global_scale[e])[: 2 * ex.inter]
+        y = ref.swiglu(a @ w13.T)
+        a2 = dequant_nvfp4_rows(*quant_nvfp4_rows(y, ex.fc2_act_scale))
+        w2 = dequant_nvfp4_rows(ex.w2.data[e], ex.w2.sf[e], ex.w2.global_scale[e])[: xf.shape[1]]
+        out.index_add_(0, tok, we * (a2 @ w2.T))
+    return out
 
 
 # ---------------------------------------------------------------------------

@@ -292,6 +292,70 @@ def moe_experts(h, w: torch.Tensor, ids: torch.Tensor, ex, out_dtype=torch.bfloa
     return out
 
 
+def nvfp4_quant(x: torch.Tensor):
+    """bf16/fp32 rows -> (packed e2m1 [T, K/2], e4m3 scales (chunk layout),
+    per-row fp32 global scale [T])."""
+    T, K = x.shape
+    dev = x.device
+    q = torch.empty(T, K // 2, dtype=torch.uint8, device=dev)
+    sf = torch.empty(round_up(max(T, 1), 128) * (K // 16), dtype=torch.uint8, device=dev)
+    g = torch.empty(T, dtype=torch.float32, device=dev)
+    _C.nvfp4_quant(x if x.stride(-1) == 1 else x.contiguous(), q, sf, g)
+    return q, sf, g
+
+
+def moe_experts_nvfp4(h, w, ids, ex, out_dtype=torch.bfloat16, n_experts_total=None, combine: bool = True):
+    """NVFP4 routed experts: per-token NVFP4 quantization of the MoE input ->
+    routing layout -> row gather -> persistent FC1 (kind::mxf4nvf4, SwiGLU,
+    NVFP4 requant) -> FC2 (routing-weighted) -> combine."""
+    from . import QAct
+    x = h.hf if isinstance(h, QAct) and h.hf is not None else (h if not isinstance(h, QAct) else None)
+    if x is None:
+        from .quant import dequant_mxfp8
+        x = dequant_mxfp8(h.q, h.sf).to(torch.bfloat16)
+    T, Hd = x.shape
+    K = ids.shape[1]
+    E = ex.count
+    dev = x.device
+    I = ex.inter
+    e_tot = n_experts_total or E
+    exp_rows = T * K / e_tot
+    bn1 = moe_tile_n(exp_rows, 64)
+    bn2 = moe_tile_n(exp_rows, 128)
+    max_rows = round_up(T * K, 128) + E * 128
+    xq, xsf, xg = nvfp4_quant(x)
+    seg_start = torch.empty(E, dtype=torch.int32, device=dev)
+    seg_count = torch.empty(E, dtype=torch.int32, device=dev)
+    tt1 = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    tt2 = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    row_token = torch.empty(max_rows, dtype=torch.int32, device=dev)
+    row_weight = torch.empty(max_rows, dtype=torch.float32, device=dev)
+    pair_row = torch.empty(T, K, dtype=torch.int32, device=dev)
+    total = torch.empty(1, dtype=torch.int32, device=dev)
+    ids = ids if ids.dtype == torch.int32 else ids.int()
+    _C.moe_align(ids.contiguous(), w.float().contiguous(), ex.first, E, seg_start, seg_count, row_token, row_weight,
+                 pair_row, total, bn1, tt1, bn2, tt2)
+    xs_q = torch.empty(max_rows, Hd // 2, dtype=torch.uint8, device=dev)
+    xs_sf = torch.empty(max_rows * (Hd // 16), dtype=torch.uint8, device=dev)
+    xs_g = torch.empty(max_rows, dtype=torch.float32, device=dev)
+    _C.moe_gather4(xq, xsf, xg, pair_row, xs_q, xs_sf, xs_g)
+    hq = torch.empty(max_rows, I // 2, dtype=torch.uint8, device=dev)
+    hsf = torch.empty(max_rows * (I // 16), dtype=torch.uint8, device=dev)
+    w13, w2 = ex.w13, ex.w2
+    g2 = float(ex.fc2_act_scale)
+    _C.gemm_grouped(w13.data, w13.sf, xs_q, xs_sf, 2 * I, Hd, E, I, bn1, seg_start, seg_count, tt1, 2,
+                    None, 0, hq, hsf, I, None, 0, True, w_g=w13.global_scale, x_g=xs_g, out_g=g2)
+    y = torch.empty(max_rows, Hd, dtype=torch.bfloat16, device=dev)
+    _C.gemm_grouped(w2.data, w2.sf, hq, hsf, Hd, I, E, 0, bn2, seg_start, seg_count, tt2, 3,
+                    y, Hd, None, None, 0, row_weight, 0, True, w_g=w2.global_scale, x_g_const=g2)
+    if not combine:
+        from . import MoEPartial
+        return MoEPartial(y, pair_row, None)
+    out = torch.empty(T, Hd, dtype=out_dtype, device=dev)
+    _C.moe_combine(y, pair_row, None, out)
+    return out
+
+
 def moe_experts_ep(h, w, ids, ex, T_step: int, n_experts_total: int, ep):
     """Expert-parallel MoE: ep_dispatch (P2P push of routed rows) -> ep_align
     (bounded wait + routing layout over all ranks' tokens) -> ep_gather ->

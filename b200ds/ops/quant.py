@@ -157,33 +157,81 @@ def _e2m1_decode(c: torch.Tensor) -> torch.Tensor:
 
 @dataclass
 class NVFP4Tensor:
-    data: torch.Tensor      # uint8 [R, K/2], low nibble = even element
-    sf: torch.Tensor        # e4m3 [R, K/16] (plain row-major)
-    global_scale: torch.Tensor  # fp32 scalar
+    """NVFP4 matrix (or a stack of E matrices): data uint8 [..., R, K/2]
+    packed e2m1 pairs (low nibble = even element); sf uint8 [..., packed] e4m3
+    scales per 16 elements in the same 128-row x 4-column chunk layout as the
+    MXFP8 scales (K/16 scale columns); global_scale fp32 [...] (per matrix).
+    ``rows`` is the logical row count when R was padded to a multiple of 128."""
+    data: torch.Tensor
+    sf: torch.Tensor
+    global_scale: torch.Tensor
+    rows: Optional[int] = None
+
+    @property
+    def shape(self):
+        d = self.data.shape
+        return (*d[:-1], d[-1] * 2)
 
     def dequant(self) -> torch.Tensor:
         return dequant_nvfp4(self.data, self.sf, self.global_scale)
 
 
+def _nvfp4_encode(x: torch.Tensor, g: torch.Tensor):
+    """x [R, K] fp32, g [R, 1] global scales -> (packed codes [R, K/2],
+    e4m3 block scales [R, K/16])."""
+    R, K = x.shape
+    xb = x.view(R, K // 16, 16)
+    amax = xb.abs().amax(-1)
+    s = (amax / (E2M1_MAX * g)).to(torch.float8_e4m3fn)
+    denom = (s.float() * g).unsqueeze(-1)
+    v = torch.where(denom > 0, xb / denom, torch.zeros_like(xb)).view(R, K)
+    codes = _e2m1_encode(v)
+    packed = (codes[:, 0::2] | (codes[:, 1::2] << 4)).to(torch.uint8)
+    return packed, s
+
+
 def quant_nvfp4_ref(x: torch.Tensor, global_scale: Optional[torch.Tensor] = None) -> NVFP4Tensor:
+    """Weight-style NVFP4: one global scale for the matrix (amax / (448*6)
+    unless given), rows padded to a multiple of 128 (zeros)."""
     R, K = x.shape
     xf = x.float()
     if global_scale is None:
         global_scale = (xf.abs().amax() / (E4M3_MAX * E2M1_MAX)).clamp(min=1e-12)
-    xb = xf.view(R, K // 16, 16)
-    amax = xb.abs().amax(-1)
-    s = (amax / (E2M1_MAX * global_scale)).to(torch.float8_e4m3fn)
-    denom = (s.float() * global_scale).unsqueeze(-1)
-    v = torch.where(denom > 0, xb / denom, torch.zeros_like(xb)).view(R, K)
-    codes = _e2m1_encode(v)
-    packed = (codes[:, 0::2] | (codes[:, 1::2] << 4)).to(torch.uint8)
-    return NVFP4Tensor(packed, s, global_scale.float().reshape(()))
+    g = global_scale.float().reshape(())
+    Rp = round_up(R, SF_ROWS)
+    if Rp != R:
+        xf = torch.cat([xf, xf.new_zeros(Rp - R, K)], 0)
+    packed, s = _nvfp4_encode(xf, g.view(1, 1).expand(Rp, 1))
+    return NVFP4Tensor(packed, pack_sf(s.view(torch.uint8)), g, R)
 
 
-def dequant_nvfp4(data: torch.Tensor, sf: torch.Tensor, g: torch.Tensor) -> torch.Tensor:
+def quant_nvfp4_rows(x: torch.Tensor, global_scale: Optional[float] = None):
+    """Activation-style NVFP4: per-row global scale g_r = amax_r / (448*6)
+    (or one fixed value).  Returns (packed [R, K/2], sf packed, g [R])."""
+    R, K = x.shape
+    xf = x.float()
+    if global_scale is None:
+        am = xf.abs().amax(-1)
+        g = torch.where(am > 0, am / (E4M3_MAX * E2M1_MAX), torch.ones_like(am))
+    else:
+        g = torch.full((R,), float(global_scale), dtype=torch.float32, device=x.device)
+    packed, s = _nvfp4_encode(xf, g.view(R, 1))
+    return packed, pack_sf(s.view(torch.uint8)), g
+
+
+def dequant_nvfp4_rows(data: torch.Tensor, sf: torch.Tensor, g: torch.Tensor) -> torch.Tensor:
+    """Inverse of quant_nvfp4_rows / quant_nvfp4_ref (g per row or scalar)."""
     R = data.shape[0]
     K = data.shape[1] * 2
     lo = _e2m1_decode(data & 0xF)
     hi = _e2m1_decode(data >> 4)
     v = torch.stack([lo, hi], -1).view(R, K)
-    return (v.view(R, K // 16, 16) * sf.float().unsqueeze(-1) * g.float()).view(R, K)
+    s = unpack_sf(sf, R, K * 2).view(torch.float8_e4m3fn).float()       # [R, K/16] (K/16 = 2K/32 columns)
+    gg = g.float().reshape(-1, 1) if g.dim() > 0 else g.float()
+    return (v.view(R, K // 16, 16) * s.unsqueeze(-1)).view(R, K) * gg
+
+
+def dequant_nvfp4(data: torch.Tensor, sf: torch.Tensor, g: torch.Tensor) -> torch.Tensor:
+    if data.dim() == 3:
+        return torch.stack([dequant_nvfp4(data[e], sf[e], g[e]) for e in range(data.shape[0])])
+    return dequant_nvfp4_rows(data, sf, g)

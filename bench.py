@@ -86,8 +86,9 @@ def parse():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="native", choices=["native", "baseline", "reference"])
     p.add_argument("--config", default="v3-1k", choices=sorted(BENCH_CONFIGS),
-                   help="named workload: v3-1k (headline: 671B, 64 x 1K), v32-sparse-32k (671B + lightning "
-                        "indexer top-2048, 8 x 32K)")
+                   help="named workload: v3-1k (headline: 671B, 64 x 1K, TP attention + EP), v32-sparse-32k "
+                        "(671B + lightning indexer top-2048, 8 x 32K), v3-dp-2k / v3-nvfp4-dp-2k (DP attention "
+                        "+ EP, 256 x 2K; MXFP8 / NVFP4 routed experts)")
     p.add_argument("--model", default=None)
     p.add_argument("--batch", type=int, default=None)
     p.add_argument("--input-len", type=int, default=None)
@@ -97,6 +98,7 @@ def parse():
     a.model = a.model or d["model"]
     a.batch = a.batch or d["batch"]
     a.input_len = a.input_len or d["input_len"]
+    a.dp = bool(d.get("dp", False))
     return a
 
 
@@ -104,6 +106,9 @@ def parse():
 BENCH_CONFIGS = {
     "v3-1k": {"model": "deepseek-v3-671b", "batch": 64, "input_len": 1024},
     "v32-sparse-32k": {"model": "deepseek-v3.2-sparse-671b", "batch": 8, "input_len": 32768},
+    # DP attention on every rank + EP over all ranks, 256 requests x 2K
+    "v3-dp-2k": {"model": "deepseek-v3-671b", "batch": 256, "input_len": 2048, "dp": True},
+    "v3-nvfp4-dp-2k": {"model": "deepseek-v3-671b-nvfp4", "batch": 256, "input_len": 2048, "dp": True},
 }
 
 
@@ -133,7 +138,7 @@ def main():
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
-    ps = init_parallel(backend="nccl", timeout_s=600)
+    ps = init_parallel(backend="nccl", timeout_s=600, dp_attention=args.dp)
     dev = ps.device if ps.device.type == "cuda" else torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     ops.set_impl("torch" if args.impl == "baseline" else "native")
@@ -141,23 +146,28 @@ def main():
         import b200ds._C  # noqa: F401
     cfg = PRESETS[args.model]()
     ctx = args.input_len + args.warmup + 2 * args.steps + 8
-    ecfg = EngineConfig(tp_size=world, ep_size=world, page_size=64, max_num_seqs=args.batch,
-                        max_prefill_tokens=16384, cuda_graphs=True, graph_batch_sizes=(args.batch,),
-                        enable_prefix_cache=False, weight_sets=args.weight_sets,
-                        max_model_len=max(16384, ctx + 64))
+    # DP attention: each rank serves batch / world of the requests
+    assert not args.dp or args.batch % world == 0, "DP attention needs batch % gpus == 0"
+    local_batch = args.batch // world if args.dp else args.batch
+    ecfg = EngineConfig(tp_size=1 if args.dp else world, ep_size=world, page_size=64, max_num_seqs=local_batch,
+                        max_prefill_tokens=16384 if not args.dp else 4096, cuda_graphs=True,
+                        graph_batch_sizes=(local_batch,), enable_prefix_cache=False, weight_sets=args.weight_sets,
+                        max_model_len=max(16384, ctx + 64), dp_attention=args.dp)
     t0 = time.time()
     log(f"building {args.model} on {world} GPU(s)")
     kv_per_tok = cfg.num_hidden_layers * (cfg.kv_cache_dim + (cfg.index_head_dim + 4 if cfg.index_n_heads else 0))
-    reserve = 24e9 + args.batch * (ctx + 64) * kv_per_tok
+    reserve = 24e9 + local_batch * (ctx + 64) * kv_per_tok
     model = build_random_model(cfg, ecfg, ps, dev, seed=0, reserve_bytes=reserve)
     torch.cuda.synchronize()
     t_init = time.time() - t0
     pages_per_seq = (ctx + ecfg.page_size - 1) // ecfg.page_size
-    eng = Engine(model, ecfg, num_pages=args.batch * pages_per_seq + 8)
+    eng = Engine(model, ecfg, num_pages=local_batch * pages_per_seq + 8)
     eng.graphs.max_pages = pages_per_seq
 
     g = torch.Generator().manual_seed(0)
     prompts = torch.randint(0, cfg.vocab_size, (args.batch, args.input_len), generator=g).tolist()
+    if args.dp:
+        prompts = prompts[ps.rank::world]
     sp = SamplingParams(max_tokens=1 << 30, ignore_eos=True)
     reqs = [eng.add_request(p, sp) for p in prompts]
 
@@ -179,7 +189,15 @@ def main():
     s0 = torch.cuda.Event(enable_timing=True)
     s1 = torch.cuda.Event(enable_timing=True)
     s0.record()
-    while any(r.t_first is None for r in reqs):
+    def pending_prefill() -> bool:
+        p = int(any(r.t_first is None for r in reqs))
+        if args.dp and world > 1:       # DP ranks step in lockstep until all are done
+            t = torch.tensor([p], dtype=torch.int64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=ps.cpu_group)
+            p = int(t.item())
+        return bool(p)
+
+    while pending_prefill():
         eng.step()
     s1.record()
     barrier()
@@ -229,8 +247,8 @@ def main():
     e2e_value = args.batch * args.steps / (e2e_ms / 1e3)
     tpot_p50 = statistics.median(step_times) * 1e3
 
-    h2d = args.batch * (4 + 4 + 8 + 4) + args.batch * eng.graphs.max_pages * 4
-    d2h = args.batch * 8
+    h2d = local_batch * (4 + 4 + 8 + 4) + local_batch * eng.graphs.max_pages * 4
+    d2h = local_batch * 8
     launches = count_launches(gr) if args.impl == "native" else None
     if os.environ.get("B200_BENCH_PROFILE") == "1":
         profile_breakdown(gr, ps.rank)
@@ -260,7 +278,8 @@ def main():
             "config": {"name": args.config, "model": args.model, "global_batch": args.batch,
                        "seq_len": args.input_len,
                        "context_during_timing": [args.input_len + args.warmup, args.input_len + args.warmup + 2 * args.steps],
-                       "parallelism": f"tp{world}-attn+ep{world}-moe", "weight_sets": getattr(model, "weight_sets", None),
+                       "parallelism": (f"dp{world}-attn+ep{world}-moe" if args.dp else f"tp{world}-attn+ep{world}-moe"),
+                       "expert_format": cfg.expert_format, "weight_sets": getattr(model, "weight_sets", None),
                        "l2": "no flush: per-step weights+KV >> 126 MB L2", "init_s": round(t_init, 1)},
         }
         print(json.dumps(out), flush=True)

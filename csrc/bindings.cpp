@@ -203,7 +203,8 @@ void gemm_grouped(const at::Tensor& w, const at::Tensor& w_sf, const at::Tensor&
                   int64_t nw, int64_t k, int64_t E, int64_t inter, int64_t bn, const at::Tensor& seg_start,
                   const at::Tensor& seg_count, const at::Tensor& ttile_off, int64_t epi, c10::optional<at::Tensor> out,
                   int64_t ldo, c10::optional<at::Tensor> q_out, c10::optional<at::Tensor> sf_out, int64_t ldq,
-                  c10::optional<at::Tensor> row_weight, int64_t num_ctas, bool pdl) {
+                  c10::optional<at::Tensor> row_weight, int64_t num_ctas, bool pdl, c10::optional<at::Tensor> w_g,
+                  c10::optional<at::Tensor> x_g, double x_g_const, double out_g) {
   check_cuda(w, "w");
   const c10::cuda::CUDAGuard g(w.device());
   TORCH_CHECK(k % 128 == 0 && nw % 128 == 0, "k and nw must be multiples of 128");
@@ -231,7 +232,33 @@ void gemm_grouped(const at::Tensor& w, const at::Tensor& w_sf, const at::Tensor&
   a.row_weight = optr<float>(row_weight);
   a.num_ctas = num_ctas > 0 ? num_ctas : num_sms();
   a.pdl = pdl ? 1 : 0;
+  a.fp4 = (w_g.has_value() && w_g->defined()) ? 1 : 0;
+  a.w_g = optr<float>(w_g);
+  a.x_g = optr<float>(x_g);
+  a.x_g_const = float(x_g_const);
+  a.out_g = float(out_g);
   check(b200_gemm_grouped(&a, cur_stream()), "gemm_grouped");
+}
+
+void nvfp4_quant(const at::Tensor& x, at::Tensor q, at::Tensor sf, at::Tensor g) {
+  check_cuda(x, "x");
+  const c10::cuda::CUDAGuard gd(x.device());
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x [T, K] unit inner stride");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 || x.scalar_type() == at::kFloat, "x bf16/fp32");
+  TORCH_CHECK(q.is_contiguous() && q.size(1) * 2 == x.size(1), "q [T, K/2] uint8");
+  check(b200_nvfp4_quant(x.data_ptr(), x.scalar_type() == at::kFloat, x.stride(0), x.size(0), x.size(1),
+                         ptr<uint8_t>(q), ptr<uint8_t>(sf), ptr<float>(g), cur_stream()),
+        "nvfp4_quant");
+}
+
+void moe_gather4(const at::Tensor& xq, const at::Tensor& xsf, const at::Tensor& xg, const at::Tensor& pair_row,
+                 at::Tensor dq, at::Tensor dsf, at::Tensor dg) {
+  check_cuda(xq, "xq");
+  const c10::cuda::CUDAGuard gd(xq.device());
+  check(b200_moe_gather4(ptr<uint8_t>(xq), ptr<uint8_t>(xsf), ptr<float>(xg), ptr<int>(pair_row), pair_row.numel(),
+                         pair_row.size(1), xq.size(1) * 2, ptr<uint8_t>(dq), ptr<uint8_t>(dsf), ptr<float>(dg),
+                         cur_stream()),
+        "moe_gather4");
 }
 
 void moe_combine(const at::Tensor& y, const at::Tensor& pair_row, c10::optional<at::Tensor> add, at::Tensor out) {
@@ -292,7 +319,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_align", &moe_align);
   m.def("moe_gather", &moe_gather);
   m.def("moe_combine", &moe_combine);
-  m.def("gemm_grouped", &gemm_grouped);
+  m.def("gemm_grouped", &gemm_grouped, pybind11::arg("w"), pybind11::arg("w_sf"), pybind11::arg("x"), pybind11::arg("x_sf"), pybind11::arg("nw"), pybind11::arg("k"), pybind11::arg("E"), pybind11::arg("inter"), pybind11::arg("bn"), pybind11::arg("seg_start"), pybind11::arg("seg_count"), pybind11::arg("ttile_off"), pybind11::arg("epi"), pybind11::arg("out"), pybind11::arg("ldo"), pybind11::arg("q_out"), pybind11::arg("sf_out"), pybind11::arg("ldq"), pybind11::arg("row_weight"), pybind11::arg("num_ctas"), pybind11::arg("pdl"),
+        pybind11::arg("w_g") = pybind11::none(), pybind11::arg("x_g") = pybind11::none(),
+        pybind11::arg("x_g_const") = 1.0, pybind11::arg("out_g") = 1.0);
+  m.def("nvfp4_quant", &nvfp4_quant);
+  m.def("moe_gather4", &moe_gather4);
   m.def("num_sms", &num_sms);
   m.def("graph_kernel_count", &graph_kernel_count);
   m.def("fill_bytes", &fill_bytes);

@@ -175,6 +175,17 @@ __host__ __device__ constexpr uint32_t idesc_mxf8(uint32_t M, uint32_t N, uint32
          | (sfa_id & 3u) << 29;      // A scale-factor id
 }
 
+// Instruction descriptor for kind::mxf4nvf4.block_scale with 16-element
+// blocks (NVFP4): A and B e2m1, K-major, UE4M3 scales, f32 accumulate; each
+// MMA (K = 64) reads the four scale bytes of its row's 32-bit TMEM word.
+__host__ __device__ constexpr uint32_t idesc_nvf4(uint32_t M, uint32_t N) {
+  return 1u << 7                     // A format e2m1
+         | 1u << 10                  // B format e2m1
+         | ((N >> 3) & 0x3Fu) << 17  // N / 8
+         | 0u << 23                  // scale format UE4M3
+         | ((M >> 4) & 0x1Fu) << 24; // M / 16
+}
+
 // Instruction descriptor for kind::f8f6f4 (no block scale): e4m3 x e4m3 -> f32.
 __host__ __device__ constexpr uint32_t idesc_f8(uint32_t M, uint32_t N, bool a_mn_major, bool b_mn_major) {
   return 1u << 4                      // D format f32
@@ -213,6 +224,29 @@ B200_DEVICE void mma_mxf8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uin
       "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
       ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
       : "memory");
+}
+
+// D(tmem) (+)= A(smem) x B(smem), NVFP4 block-scaled (e2m1, e4m3 scale per 16).
+B200_DEVICE void mma_nvf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t sfa_tmem,
+                          uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+// Two floats -> packed e2m1 pair (round to nearest even, saturating): lo in
+// bits 0-3, hi in bits 4-7.
+B200_DEVICE uint32_t f2_to_e2m1x2(float lo, float hi) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .b8 b;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b, %2, %1;\n\t"
+      "cvt.u32.u8 %0, b;\n\t}"
+      : "=r"(r) : "f"(lo), "f"(hi));
+  return r & 0xFFu;
 }
 
 // D(tmem) (+)= A(smem) x B(smem), e4m3 without block scales.

@@ -21,3 +21,9 @@ int b200_moe_gather(const uint8_t* xq, const uint8_t* xsf, const int* pair_row, 
 int b200_moe_combine(const void* y, const int* pair_row, int T, int K, int D, const void* add, int add_f32, void* out,
                      int out_f32, cudaStream_t st);
 int b200_fill_bytes(void* p, int64_t nbytes, uint64_t seed, uint8_t and_mask, uint8_t or_mask, cudaStream_t st);
+
+// NVFP4 activations (see nvfp4.cu).
+int b200_nvfp4_quant(const void* x, int f32, int64_t ld, int T, int K, uint8_t* q, uint8_t* sf, float* g,
+                     cudaStream_t st);
+int b200_moe_gather4(const uint8_t* xq, const uint8_t* xsf, const float* xg, const int* pair_row, int npairs, int K,
+                     int Kx, uint8_t* dq, uint8_t* dsf, float* dg, cudaStream_t st);

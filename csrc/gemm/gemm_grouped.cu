@@ -12,6 +12,13 @@
 //                           scale block
 //   FC2 (kEpiWeightedBf16): y[r] = bf16(routing_weight[r] * (h Wd^T)[r])
 //
+// NVFP4 variant (FP4 = true, kind::mxf4nvf4 with 16-element e4m3 scales):
+// the same 128-byte k-tiles now hold 256 e2m1 elements (4 MMAs of K = 64),
+// each MMA reads its own 512-byte scale chunk (4 per k-tile and operand,
+// staged through a 4-slot TMEM ring), the epilogue applies the fp32 global
+// scales (per expert x per token row), and FC1 requantizes its SwiGLU output
+// to NVFP4 (16-channel blocks = 16 lanes of an epilogue warp).
+//
 // The tile list comes from the routing-layout kernel: ttile_off[e] is the
 // prefix sum over experts of ceil(count_e / BN).  All waits are bounded.
 //
@@ -28,18 +35,26 @@ constexpr int kTileM = 128;
 constexpr int kTileK = 128;
 constexpr int kSf = 512;
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool FP4>
 struct Cfg {
   static constexpr int kA = (EPI == kEpiSwiglu) ? 2 : 1;
-  static constexpr int kLoadBytes = kA * kTileM * kTileK + BN * kTileK + kA * kSf + kSf;   // TMA bytes per stage
-  static constexpr int kStageBytes = kLoadBytes + kSf;    // + padding after the activation scale chunk
-  static constexpr int kStages0 = (200 * 1024) / kStageBytes;
-  static constexpr int kStages = kStages0 > 16 ? 16 : kStages0;
+  static constexpr int kSfK = FP4 ? 4 * kSf : kSf;          // scale bytes per 128 rows per k-tile
+  static constexpr int kLoadBytes = kA * kTileM * kTileK + BN * kTileK + kA * kSfK + kSfK;   // TMA bytes per stage
+  static constexpr int kStageBytes = kLoadBytes + kSfK;   // + padding after the activation scale chunks
   static constexpr int kAcc = kA * BN;                      // columns per accumulator buffer
-  static constexpr int kSfCols = kStages * (4 * kA + 4);
+  static constexpr int kSlotCols = FP4 ? 16 * kA + 16 : 4 * kA + 4;   // scale columns per stage
+  // Stages bounded by shared memory and by TMEM (one scale slot per stage, so
+  // a slot is rewritten only after its stage's MMAs released the stage).
+  static constexpr int kStagesSmem = (200 * 1024) / kStageBytes;
+  static constexpr int kStagesTmem = (512 - 2 * kAcc) / kSlotCols;
+  static constexpr int kStages0 = kStagesSmem < kStagesTmem ? kStagesSmem : kStagesTmem;
+  static constexpr int kStages = kStages0 > 16 ? 16 : kStages0;
+  static constexpr int kSfSlots = kStages;
+  static constexpr int kSfCols = kSfSlots * kSlotCols;
   static constexpr int kNeed = 2 * kAcc + kSfCols;
   static constexpr int kTmemCols = kNeed <= 32 ? 32 : kNeed <= 64 ? 64 : kNeed <= 128 ? 128 : kNeed <= 256 ? 256 : 512;
   static_assert(kNeed <= 512, "TMEM budget");
+  static_assert(kStages >= 2, "pipeline depth");
   static constexpr int kSmem = kStages * kStageBytes + 1024 + 512;
 };
 
@@ -62,6 +77,10 @@ struct Params {
   int inter;
   const float* row_weight;
   uint32_t* err;
+  const float* w_g;          // NVFP4: per-expert global scale
+  const float* x_g;          // NVFP4: per-row activation global scale (or null)
+  float x_g_const;
+  float out_g;               // NVFP4 FC1: global scale of the requantized output
 };
 
 __device__ __forceinline__ int64_t sf_offset(int row, int kblock, int kb_total) {
@@ -95,17 +114,17 @@ __device__ __forceinline__ Tile map_tile(const Params& p, const int* lay, int w)
   return t;
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool FP4>
 __global__ void __launch_bounds__(kThreads, 1)
 grouped_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, Params p) {
-  using C = Cfg<BN, EPI>;
+  using C = Cfg<BN, EPI, FP4>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = sA + C::kStages * C::kA * kTileM * kTileK;
   uint8_t* sSFA = sB + C::kStages * BN * kTileK;
-  uint8_t* sSFB = sSFA + C::kStages * C::kA * kSf;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sSFB + C::kStages * 2 * kSf);
+  uint8_t* sSFB = sSFA + C::kStages * C::kA * C::kSfK;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sSFB + C::kStages * 2 * C::kSfK);
   uint64_t* empty = full + C::kStages;
   uint64_t* acc_full = empty + C::kStages;    // [2]
   uint64_t* acc_empty = acc_full + 2;         // [2]
@@ -147,8 +166,10 @@ grouped_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
   }
   __syncthreads();
   const int total = lay[p.E] * p.n_tiles;
-  const int nk = p.k / kTileK;
-  const int kc_total = p.k / kTileK;           // 512-byte sf chunks per 128 rows
+  const int kbytes = FP4 ? p.k / 2 : p.k;      // operand bytes per row
+  const int nk = kbytes / kTileK;
+  const int kc_total = FP4 ? p.k / 64 : p.k / kTileK;   // 512-byte sf chunks per 128 rows
+  constexpr int kChunksPerTile = FP4 ? 4 : 1;
 
   if (warp == 0) {
     // ------------------------------ producer ------------------------------
@@ -173,14 +194,16 @@ grouped_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
           if (EPI == kEpiSwiglu)
             tma_load_2d_hint(a_dst + kTileM * kTileK, &tm_a, &full[s], kt * kTileK, a_row + p.inter, pol_w);
           tma_load_2d_hint(sB + (size_t)s * BN * kTileK, &tm_b, &full[s], kt * kTileK, b_row, pol_x);
-          uint8_t* sfa_dst = sSFA + (size_t)s * C::kA * kSf;
-          bulk_load_hint(sfa_dst, sfa_e + ((int64_t)(t.tile_n * kc_total + kt) << 9), kSf, &full[s], pol_w);
+          uint8_t* sfa_dst = sSFA + (size_t)s * C::kA * C::kSfK;
+          const int kc0 = kt * kChunksPerTile;
+          bulk_load_hint(sfa_dst, sfa_e + ((int64_t)(t.tile_n * kc_total + kc0) << 9), C::kSfK, &full[s], pol_w);
           if (EPI == kEpiSwiglu) {
             const int rb_up = (p.inter + t.tile_n * kTileM) >> 7;
-            bulk_load_hint(sfa_dst + kSf, sfa_e + ((int64_t)(rb_up * kc_total + kt) << 9), kSf, &full[s], pol_w);
+            bulk_load_hint(sfa_dst + C::kSfK, sfa_e + ((int64_t)(rb_up * kc_total + kc0) << 9), C::kSfK, &full[s],
+                           pol_w);
           }
-          bulk_load_hint(sSFB + (size_t)s * 2 * kSf, p.sfb + ((int64_t)((b_row >> 7) * kc_total + kt) << 9), kSf,
-                         &full[s], pol_x);
+          bulk_load_hint(sSFB + (size_t)s * 2 * C::kSfK, p.sfb + ((int64_t)((b_row >> 7) * kc_total + kc0) << 9),
+                         C::kSfK, &full[s], pol_x);
         }
       }
     }
@@ -204,23 +227,29 @@ grouped_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
         // repacks them into a tile-local chunk (row j -> line j % 32, byte
         // group j / 32) so the MMA always reads scales at the base column.
         const int o = b_row & 127;
-        uint8_t* sfb_stage = sSFB + (size_t)s * 2 * kSf;
+        uint8_t* sfb_stage = sSFB + (size_t)s * 2 * C::kSfK;
         if (o != 0) {
-          for (int j = lane; j < BN; j += 32) {
-            const int r = o + j;
-            const uint32_t v = *reinterpret_cast<const uint32_t*>(sfb_stage + (r & 31) * 16 + (r >> 5) * 4);
-            *reinterpret_cast<uint32_t*>(sfb_stage + kSf + (j & 31) * 16 + (j >> 5) * 4) = v;
-          }
+          for (int ch = 0; ch < kChunksPerTile; ++ch)
+            for (int j = lane; j < BN; j += 32) {
+              const int r = o + j;
+              const uint32_t v =
+                  *reinterpret_cast<const uint32_t*>(sfb_stage + ch * kSf + (r & 31) * 16 + (r >> 5) * 4);
+              *reinterpret_cast<uint32_t*>(sfb_stage + C::kSfK + ch * kSf + (j & 31) * 16 + (j >> 5) * 4) = v;
+            }
           fence_proxy_async_smem();
           __syncwarp();
         }
         if (lane == 0) {
-          const uint32_t sf_a = tmem_sf + s * (4 * C::kA + 4);
-          const uint32_t sf_b = sf_a + 4 * C::kA;
-          const uint8_t* sfa_src = sSFA + (size_t)s * C::kA * kSf;
+          const uint32_t sf_a = tmem_sf + (it % C::kSfSlots) * C::kSlotCols;
+          const uint32_t sf_b = sf_a + 4 * kChunksPerTile * C::kA;
+          const uint8_t* sfa_src = sSFA + (size_t)s * C::kA * C::kSfK;
+          const uint8_t* sfb_src = sfb_stage + (o != 0 ? C::kSfK : 0);
           for (int a = 0; a < C::kA; ++a)
-            tmem_cp_32x128b_x4(sf_a + 4 * a, smem_desc(smem_u32(sfa_src + a * kSf), 0, 128, 0));
-          tmem_cp_32x128b_x4(sf_b, smem_desc(smem_u32(sfb_stage + (o != 0 ? kSf : 0)), 0, 128, 0));
+            for (int ch = 0; ch < kChunksPerTile; ++ch)
+              tmem_cp_32x128b_x4(sf_a + 4 * (a * kChunksPerTile + ch),
+                                 smem_desc(smem_u32(sfa_src + a * C::kSfK + ch * kSf), 0, 128, 0));
+          for (int ch = 0; ch < kChunksPerTile; ++ch)
+            tmem_cp_32x128b_x4(sf_b + 4 * ch, smem_desc(smem_u32(sfb_src + ch * kSf), 0, 128, 0));
           const uint32_t a_base = smem_u32(sA + (size_t)s * C::kA * kTileM * kTileK);
           const uint32_t b_base = smem_u32(sB + (size_t)s * BN * kTileK);
           for (int kk = 0; kk < kTileK / 32; ++kk) {
@@ -228,8 +257,14 @@ grouped_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
             const uint32_t accf = (kt > 0 || kk > 0) ? 1u : 0u;
             for (int a = 0; a < C::kA; ++a) {
               const uint64_t adesc = desc_kmajor_sw128(a_base + a * kTileM * kTileK + kk * 32);
-              mma_mxf8(acc + a * BN, adesc, bdesc, idesc_mxf8(kTileM, BN, kk, kk),
-                       (sf_a + 4 * a) | (uint32_t(kk) << 30), sf_b | (uint32_t(kk) << 30), accf);
+              if constexpr (FP4) {
+                // MMA kk (64 elements) reads scale chunk kk: its own 4 columns
+                mma_nvf4(acc + a * BN, adesc, bdesc, idesc_nvf4(kTileM, BN),
+                         sf_a + 4 * (a * kChunksPerTile + kk), sf_b + 4 * kk, accf);
+              } else {
+                mma_mxf8(acc + a * BN, adesc, bdesc, idesc_mxf8(kTileM, BN, kk, kk),
+                         (sf_a + 4 * a) | (uint32_t(kk) << 30), sf_b | (uint32_t(kk) << 30), accf);
+              }
             }
           }
           mma_commit(&empty[s]);
@@ -254,7 +289,40 @@ grouped_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
       const int tmax = t.rows - t.tt * BN;
       const int wrow = t.tile_n * kTileM + sub * 32 + lane;
       const uint32_t lane_addr = tmem + buf * C::kAcc + (uint32_t(sub * 32) << 16);
-      if constexpr (EPI == kEpiSwiglu) {
+      const float wg = FP4 ? __ldg(p.w_g + t.e) : 1.f;
+      if constexpr (FP4 && EPI == kEpiSwiglu) {
+        // h = silu(g) * u with both scaled by the global scales; NVFP4 out:
+        // one 16-channel block per half-warp, two channels per byte.
+        const float inv_og = 1.f / p.out_g;
+        const int kb16 = p.inter / 16;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          uint32_t g[16], u[16];
+          tmem_ld_x16(lane_addr + c0, g);
+          tmem_ld_x16(lane_addr + BN + c0, u);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int orow = b_row + c0 + j;
+            const float sc = wg * (p.x_g ? __ldcg(p.x_g + orow) : p.x_g_const);
+            const float gv = __uint_as_float(g[j]) * sc;
+            const float h = gv / (1.0f + __expf(-gv)) * (__uint_as_float(u[j]) * sc);
+            float amax = fabsf(h);
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            const uint16_t s2 = f2_to_e4m3x2(amax * (1.f / 6.f) * inv_og, 0.f);
+            __nv_fp8_e4m3 s8;
+            s8.__x = uint8_t(s2 & 0xFF);
+            const float sf = float(s8);
+            const float v = sf > 0.f ? h * inv_og / sf : 0.f;
+            const float vn = __shfl_down_sync(0xffffffffu, v, 1);
+            if (c0 + j < tmax) {
+              if ((lane & 1) == 0) p.q_out[(int64_t)orow * (p.ldq / 2) + (wrow >> 1)] = uint8_t(f2_to_e2m1x2(v, vn));
+              if ((lane & 15) == 0) p.sf_out[sf_offset(orow, wrow >> 4, kb16)] = uint8_t(s2 & 0xFF);
+            }
+          }
+        }
+      } else if constexpr (EPI == kEpiSwiglu) {
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 16) {
           uint32_t g[16], u[16];
@@ -286,7 +354,8 @@ grouped_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
           for (int j = 0; j < 16; ++j) {
             if (c0 + j < tmax) {
               const int orow = b_row + c0 + j;
-              const float v = __uint_as_float(r[j]) * __ldcg(p.row_weight + orow);
+              float v = __uint_as_float(r[j]) * __ldcg(p.row_weight + orow);
+              if (FP4) v *= wg * (p.x_g ? __ldcg(p.x_g + orow) : p.x_g_const);
               reinterpret_cast<__nv_bfloat16*>(p.out)[(int64_t)orow * p.ldo + wrow] = __float2bfloat16(v);
             }
           }
@@ -328,12 +397,13 @@ static int map_u8(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, 
   return r == CUDA_SUCCESS ? 0 : int(r);
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool FP4>
 static int launch(const GroupedArgs& a, cudaStream_t st) {
-  using C = Cfg<BN, EPI>;
+  using C = Cfg<BN, EPI, FP4>;
   CUtensorMap ma, mb;
-  if (map_u8(&ma, a.w, (int64_t)a.E * a.nw, a.k, kTileM)) return -2;
-  if (map_u8(&mb, a.x, a.x_rows, a.k, BN)) return -3;
+  const int kbytes = FP4 ? a.k / 2 : a.k;
+  if (map_u8(&ma, a.w, (int64_t)a.E * a.nw, kbytes, kTileM)) return -2;
+  if (map_u8(&mb, a.x, a.x_rows, kbytes, BN)) return -3;
   Params p{};
   p.sfa = a.w_sf;
   p.sfa_estride = a.w_sf_estride;
@@ -353,7 +423,11 @@ static int launch(const GroupedArgs& a, cudaStream_t st) {
   p.inter = a.inter;
   p.row_weight = a.row_weight;
   p.err = a.err;
-  auto kern = grouped_kernel<BN, EPI>;
+  p.w_g = a.w_g;
+  p.x_g = a.x_g;
+  p.x_g_const = a.x_g_const;
+  p.out_g = a.out_g;
+  auto kern = grouped_kernel<BN, EPI, FP4>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.num_ctas);
@@ -368,14 +442,14 @@ static int launch(const GroupedArgs& a, cudaStream_t st) {
   return cudaLaunchKernelEx(&cfg, kern, ma, mb, p) == cudaSuccess ? 0 : 1;
 }
 
-template <int EPI>
+template <int EPI, bool FP4>
 static int launch_bn(const GroupedArgs& a, cudaStream_t st) {
   switch (a.bn) {
-    case 16: return launch<16, EPI>(a, st);
-    case 32: return launch<32, EPI>(a, st);
-    case 64: return launch<64, EPI>(a, st);
+    case 16: return launch<16, EPI, FP4>(a, st);
+    case 32: return launch<32, EPI, FP4>(a, st);
+    case 64: return launch<64, EPI, FP4>(a, st);
     case 128:
-      if constexpr (EPI != kEpiSwiglu) return launch<128, EPI>(a, st);
+      if constexpr (EPI != kEpiSwiglu) return launch<128, EPI, FP4>(a, st);
       return -4;
   }
   return -4;
@@ -387,7 +461,13 @@ static int launch_bn(const GroupedArgs& a, cudaStream_t st) {
 int b200_gemm_grouped(const GroupedArgs* a, cudaStream_t st) {
   using namespace b200::ggemm;
   if (a->k % 128 || a->nw % 128 || a->num_ctas <= 0 || a->E > b200::ggemm::kMaxExperts) return -1;
-  if (a->epi == kEpiSwiglu) return launch_bn<kEpiSwiglu>(*a, st);
-  if (a->epi == kEpiWeightedBf16) return launch_bn<kEpiWeightedBf16>(*a, st);
+  if (a->fp4) {
+    if (a->k % 256 || !a->w_g || (a->epi == kEpiSwiglu && (a->out_g <= 0.f || a->inter % 128))) return -1;
+    if (a->epi == kEpiSwiglu) return launch_bn<kEpiSwiglu, true>(*a, st);
+    if (a->epi == kEpiWeightedBf16) return launch_bn<kEpiWeightedBf16, true>(*a, st);
+    return -5;
+  }
+  if (a->epi == kEpiSwiglu) return launch_bn<kEpiSwiglu, false>(*a, st);
+  if (a->epi == kEpiWeightedBf16) return launch_bn<kEpiWeightedBf16, false>(*a, st);
   return -5;
 }

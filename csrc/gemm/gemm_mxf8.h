@@ -72,5 +72,15 @@ struct GroupedArgs {
   uint32_t* err;
   int num_ctas;
   int pdl;
+  // NVFP4 operands (fp4 = 1): w / x hold packed e2m1 pairs (k / 2 bytes per
+  // row, low nibble = even element), w_sf / x_sf e4m3 scales per 16 elements
+  // in the same 128-row x 4-column chunk layout; fp32 global scales: w_g per
+  // expert, x_g per sorted activation row (or x_g_const when null); FC1
+  // writes its SwiGLU output as NVFP4 with global scale out_g.
+  int fp4;
+  const float* w_g;
+  const float* x_g;
+  float x_g_const;
+  float out_g;
 };
 int b200_gemm_grouped(const GroupedArgs* args, cudaStream_t stream);

@@ -380,3 +380,89 @@ def test_mla_tc_sparse_matches_reference(H, lens):
     got = cuda.mla_attention(q_abs.to(DEV), q_pe.to(DEV), cache.to(DEV), 0.7, fb, 0.0625, 64, topk.to(DEV))
     exp = ref.mla_attention(q_abs, q_pe, cache, 0.7, bt, torch.tensor(lens), q_seq, q_pos, 0.0625, 64, topk)
     assert rel_err(got.cpu(), exp) < 3e-2
+
+
+# ---------------------------------------------------------------------------
+# NVFP4 routed experts (kind::mxf4nvf4)
+# ---------------------------------------------------------------------------
+
+def _nvfp4_stack(E, N, K, scale=0.05):
+    from b200ds.ops.quant import NVFP4Tensor, quant_nvfp4_ref
+    ws = [quant_nvfp4_ref(torch.randn(N, K) * scale) for _ in range(E)]
+    return NVFP4Tensor(torch.stack([w.data for w in ws]).to(DEV), torch.stack([w.sf for w in ws]).to(DEV),
+                       torch.stack([w.global_scale.reshape(()) for w in ws]).to(DEV), N)
+
+
+def test_nvfp4_quant_matches_reference():
+    from b200ds.ops import cuda
+    from b200ds.ops.quant import dequant_nvfp4_rows, quant_nvfp4_rows
+    x = (torch.randn(70, 1024) * torch.rand(70, 1) * 4).to(torch.bfloat16)
+    q, sf, g = cuda.nvfp4_quant(x.to(DEV))
+    rq, rsf, rg = quant_nvfp4_rows(x.float())
+    assert torch.allclose(g.cpu(), rg, rtol=1e-6)
+    got = dequant_nvfp4_rows(q.cpu(), sf.cpu(), g.cpu())
+    exp = dequant_nvfp4_rows(rq, rsf, rg)
+    assert rel_err(got, exp) < 1e-2
+    # the kernel forms g and the block scales with reciprocal multiplies, the
+    # reference with divisions: a 1-ulp difference can move an e4m3 block
+    # scale across a rounding midpoint and re-round that block's codes
+    assert (q.cpu() == rq).float().mean() > 0.9
+
+
+@pytest.mark.parametrize("T,bn2", [(37, None), (300, None)])
+def test_grouped_nvfp4_weighted_exact(T, bn2):
+    """NVFP4 grouped GEMM (weighted epilogue) vs fp32 math on the same
+    dequantized operands: checks the e2m1 operand / e4m3 scale layouts, the
+    per-MMA scale chunks and the global scales."""
+    from b200ds import _C
+    from b200ds.ops import cuda
+    from b200ds.ops.quant import dequant_nvfp4_rows
+    H, N, E, K = 1024, 512, 8, 4
+    w = _nvfp4_stack(E, N, H)
+    x = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    xq, xsf, xg = cuda.nvfp4_quant(x)
+    ids = torch.stack([torch.randperm(E, device=DEV)[:K] for _ in range(T)]).int()
+    wts = torch.rand(T, K, device=DEV)
+    max_rows = cuda.round_up(T * K, 128) + E * 128
+    seg_start = torch.empty(E, dtype=torch.int32, device=DEV)
+    seg_count = torch.empty(E, dtype=torch.int32, device=DEV)
+    tt1 = torch.empty(E + 1, dtype=torch.int32, device=DEV)
+    tt2 = torch.empty(E + 1, dtype=torch.int32, device=DEV)
+    row_token = torch.empty(max_rows, dtype=torch.int32, device=DEV)
+    row_weight = torch.empty(max_rows, dtype=torch.float32, device=DEV)
+    pair_row = torch.empty(T, K, dtype=torch.int32, device=DEV)
+    total = torch.empty(1, dtype=torch.int32, device=DEV)
+    bn = cuda.moe_tile_n(T * K / E, 128)
+    _C.moe_align(ids, wts, 0, E, seg_start, seg_count, row_token, row_weight, pair_row, total, 64, tt1, bn, tt2)
+    xs_q = torch.zeros(max_rows, H // 2, dtype=torch.uint8, device=DEV)
+    xs_sf = torch.zeros(max_rows * (H // 16), dtype=torch.uint8, device=DEV)
+    xs_g = torch.zeros(max_rows, dtype=torch.float32, device=DEV)
+    _C.moe_gather4(xq, xsf, xg, pair_row, xs_q, xs_sf, xs_g)
+    y = torch.zeros(max_rows, N, dtype=torch.bfloat16, device=DEV)
+    _C.gemm_grouped(w.data, w.sf, xs_q, xs_sf, N, H, E, 0, bn, seg_start, seg_count, tt2, 3,
+                    y, N, None, None, 0, row_weight, 0, True, w_g=w.global_scale, x_g=xs_g)
+    xd = dequant_nvfp4_rows(xq.cpu(), xsf.cpu(), xg.cpu())
+    pr, ss = pair_row.cpu(), seg_start.cpu()
+    for e in range(E):
+        wd = dequant_nvfp4_rows(w.data[e].cpu(), w.sf[e].cpu(), w.global_scale[e].cpu())
+        for t, k in (ids.cpu() == e).nonzero().tolist()[:20]:
+            r = int(pr[t, k])
+            exp = (xd[t] @ wd.T) * float(wts[t, k])
+            assert rel_err(y[r].cpu(), exp) < 1e-2, (e, t, rel_err(y[r].cpu(), exp))
+
+
+@pytest.mark.parametrize("T", [5, 37, 200])
+def test_moe_experts_nvfp4(T):
+    from b200ds.ops import ExpertWeights, cuda
+    from b200ds.ops.quant import NVFP4Tensor
+    import b200ds.ops as ops
+    H, I, E, K = 1024, 256, 16, 4
+    ex = ExpertWeights(8, E, _nvfp4_stack(E, 2 * I, H), _nvfp4_stack(E, H, I), I)
+    x = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    ids = torch.stack([torch.randperm(32, device=DEV)[:K] for _ in range(T)]).int()
+    wts = torch.rand(T, K, device=DEV)
+    got = cuda.moe_experts_nvfp4(x, wts, ids, ex, torch.float32)
+    cpu = lambda t: NVFP4Tensor(t.data.cpu(), t.sf.cpu(), t.global_scale.cpu(), t.rows)
+    exc = ExpertWeights(8, E, cpu(ex.w13), cpu(ex.w2), I)
+    exp = ops.moe_experts(x.float().cpu(), wts.cpu(), ids.cpu(), exc, torch.float32)
+    assert rel_err(got.cpu(), exp) < 5e-2, rel_err(got.cpu(), exp)
