@@ -362,11 +362,19 @@ def moe_experts_ep(h, w, ids, ex, T_step: int, n_experts_total: int, ep):
     persistent FC1 (SwiGLU + requant) -> FC2 (routing-weighted); the combine
     + reduce-scatter runs fused in the following norm step."""
     from . import EPPartial, QAct
-    a = h if isinstance(h, QAct) else quant(h)
-    T_r, Hd = a.q.shape
+    from .quant import NVFP4Tensor
+    fp4 = isinstance(ex.w13, NVFP4Tensor)
+    if fp4:
+        x = h.hf if isinstance(h, QAct) and h.hf is not None else h
+        q, sf, g = nvfp4_quant(x)
+        T_r, Hd = x.shape
+    else:
+        a = h if isinstance(h, QAct) else quant(h)
+        q, sf, g = a.q, a.sf, None
+        T_r, Hd = a.q.shape
     K = ids.shape[1]
     E = ex.count
-    dev = a.q.device
+    dev = q.device
     I = ex.inter
     Tg = ep.world * T_step
     exp_rows = Tg * K / n_experts_total
@@ -374,8 +382,8 @@ def moe_experts_ep(h, w, ids, ex, T_step: int, n_experts_total: int, ep):
     bn2 = moe_tile_n(exp_rows, 128)
     max_rows = round_up(Tg * K, 128) + E * 128
     ids = (ids if ids.dtype == torch.int32 else ids.int()).contiguous()
-    _C.ep_dispatch(a.q, a.sf, ids, w.float().contiguous(), T_step, n_experts_total // ep.world, ep.bases, ep.rank,
-                   ep.max_t, ep.epoch, ep.push_ticket)
+    _C.ep_dispatch(q, sf, g, Hd, ids, w.float().contiguous(), T_step, n_experts_total // ep.world, ep.bases,
+                   ep.rank, ep.max_t, ep.epoch, ep.push_ticket)
     seg_start = torch.empty(E, dtype=torch.int32, device=dev)
     seg_count = torch.empty(E, dtype=torch.int32, device=dev)
     tt1 = torch.empty(E + 1, dtype=torch.int32, device=dev)
@@ -386,13 +394,28 @@ def moe_experts_ep(h, w, ids, ex, T_step: int, n_experts_total: int, ep):
     total = torch.empty(1, dtype=torch.int32, device=dev)
     _C.ep_align(ep.bases, ep.rank, ep.max_t, Hd, K, T_step, ex.first, E, seg_start, seg_count, row_token, row_weight,
                 pair_row, total, bn1, tt1, bn2, tt2, ep.epoch, ep.err)
-    xs = alloc_qact(max_rows, Hd, dev)
-    _C.ep_gather(ep.bases, ep.rank, ep.max_t, Hd, K, T_step, pair_row, xs.q, xs.sf, ep.epoch, ep.gather_ticket)
-    hq = alloc_qact(max_rows, I, dev)
     w13, w2 = ex.w13, ex.w2
+    y = torch.empty(max_rows, Hd, dtype=torch.bfloat16, device=dev)
+    if fp4:
+        xs_q = torch.empty(max_rows, Hd // 2, dtype=torch.uint8, device=dev)
+        xs_sf = torch.empty(max_rows * (Hd // 16), dtype=torch.uint8, device=dev)
+        xs_g = torch.empty(max_rows, dtype=torch.float32, device=dev)
+        _C.ep_gather(ep.bases, ep.rank, ep.max_t, Hd, K, T_step, pair_row, xs_q, xs_sf, xs_g, ep.epoch,
+                     ep.gather_ticket)
+        hq = torch.empty(max_rows, I // 2, dtype=torch.uint8, device=dev)
+        hsf = torch.empty(max_rows * (I // 16), dtype=torch.uint8, device=dev)
+        g2 = float(ex.fc2_act_scale)
+        _C.gemm_grouped(w13.data, w13.sf, xs_q, xs_sf, 2 * I, Hd, E, I, bn1, seg_start, seg_count, tt1, 2,
+                        None, 0, hq, hsf, I, None, 0, True, w_g=w13.global_scale, x_g=xs_g, out_g=g2)
+        _C.gemm_grouped(w2.data, w2.sf, hq, hsf, Hd, I, E, 0, bn2, seg_start, seg_count, tt2, 3,
+                        y, Hd, None, None, 0, row_weight, 0, True, w_g=w2.global_scale, x_g_const=g2)
+        return EPPartial(y, pair_row, T_step, T_r)
+    xs = alloc_qact(max_rows, Hd, dev)
+    _C.ep_gather(ep.bases, ep.rank, ep.max_t, Hd, K, T_step, pair_row, xs.q, xs.sf, None, ep.epoch,
+                 ep.gather_ticket)
+    hq = alloc_qact(max_rows, I, dev)
     _C.gemm_grouped(w13.data, w13.sf, xs.q, xs.sf, 2 * I, Hd, E, I, bn1, seg_start, seg_count, tt1, 2,
                     None, 0, hq.q, hq.sf, I, None, 0, True)
-    y = torch.empty(max_rows, Hd, dtype=torch.bfloat16, device=dev)
     _C.gemm_grouped(w2.data, w2.sf, hq.q, hq.sf, Hd, I, E, 0, bn2, seg_start, seg_count, tt2, 3,
                     y, Hd, None, None, 0, row_weight, 0, True)
     return EPPartial(y, pair_row, T_step, T_r)

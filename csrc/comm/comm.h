@@ -32,10 +32,13 @@ int b200_moe_combine_push(const void* y, const int* pair_row, int T, int K, int 
 // Expert-parallel dispatch buffer (symmetric, identical layout on every rank):
 //   [0, 256)              uint32 arrival counters cnt[2][kArMaxRanks]
 //   [kEpRegionOff + p * par_bytes, ...)   parity-p region:
-//       q   e4m3 [rows_p, hidden]        rows_p = round_up(world * max_t, 128)
-//       sf  UE8M0 [rows_p * hidden / 32] (tcgen05 scale layout)
+//       q   [rows_p, hidden] bytes       rows_p = round_up(world * max_t, 128);
+//                                        MXFP8 rows use all of it, NVFP4 half
+//       sf  [rows_p * hidden / 16]       UE8M0 per 32 (MXFP8) or e4m3 per 16
+//                                        (NVFP4), tcgen05 scale layout
 //       ids int32 [world * max_t, K]     (-1 = no expert / padded token)
 //       w   fp32  [world * max_t, K]
+//       g   fp32  [world * max_t]        NVFP4 per-row global scale
 // Row (src, t) of a step with T_step tokens per rank is src * T_step + t.
 constexpr int64_t kEpRegionOff = 1024;
 
@@ -46,33 +49,35 @@ struct EpPeers {
   int max_t;
   int hidden;
   int K;
-  int64_t par_bytes, off_sf, off_ids, off_w;
+  int64_t par_bytes, off_sf, off_ids, off_w, off_g;
 };
 
 inline int64_t ep_round(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 
 inline void ep_layout(int world, int max_t, int hidden, int K, int64_t* par_bytes, int64_t* off_sf, int64_t* off_ids,
-                      int64_t* off_w) {
+                      int64_t* off_w, int64_t* off_g) {
   const int64_t rows = (int64_t)world * max_t;
   const int64_t rows_p = ep_round(rows, 128);
   *off_sf = ep_round(rows_p * hidden, 1024);
-  *off_ids = ep_round(*off_sf + rows_p * hidden / 32, 1024);
+  *off_ids = ep_round(*off_sf + rows_p * hidden / 16, 1024);
   *off_w = ep_round(*off_ids + rows * K * 4, 1024);
-  *par_bytes = ep_round(*off_w + rows * K * 4, 1024);
+  *off_g = ep_round(*off_w + rows * K * 4, 1024);
+  *par_bytes = ep_round(*off_g + rows * 4, 1024);
 }
 
 inline int64_t ep_buffer_bytes(int world, int max_t, int hidden, int K) {
-  int64_t pb, a, b, c;
-  ep_layout(world, max_t, hidden, K, &pb, &a, &b, &c);
+  int64_t pb, a, b, c, d;
+  ep_layout(world, max_t, hidden, K, &pb, &a, &b, &c, &d);
   return kEpRegionOff + 2 * pb;
 }
 
 // Dispatch: token t of this rank (T_r valid of T_step rows) goes, with its
 // routing, to every rank that owns one of its experts (routing rows go to
 // every rank, so receivers see -1 for tokens they do not serve).
-int b200_ep_dispatch(const uint8_t* q, const uint8_t* sf, const int* ids, const float* w, int T_r, int T_step,
-                     int experts_per_rank, const EpPeers* peers, const uint32_t* epoch, uint32_t* ticket,
-                     cudaStream_t st);
+// fp4 = 1: q / sf / g are NVFP4 rows (hidden / 2 bytes, e4m3 per 16, global g).
+int b200_ep_dispatch(const uint8_t* q, const uint8_t* sf, const float* g, int fp4, const int* ids, const float* w,
+                     int T_r, int T_step, int experts_per_rank, const EpPeers* peers, const uint32_t* epoch,
+                     uint32_t* ticket, cudaStream_t st);
 // Routing layout over the received world * T_step tokens (waits for every
 // rank's dispatch; bounded).
 int b200_ep_align(const EpPeers* peers, int T_step, int first, int E, int* seg_start, int* seg_count, int* row_token,
@@ -80,8 +85,8 @@ int b200_ep_align(const EpPeers* peers, int T_step, int first, int E, int* seg_s
                   const uint32_t* epoch, uint32_t* err, cudaStream_t st);
 // Gather received rows into the expert-sorted operand; the last CTA frees
 // the parity (counters to zero, epoch + 1).
-int b200_ep_gather(const EpPeers* peers, int T_step, const int* pair_row, uint8_t* dq, uint8_t* dsf, uint32_t* epoch,
-                   uint32_t* ticket, cudaStream_t st);
+int b200_ep_gather(const EpPeers* peers, int T_step, const int* pair_row, int fp4, uint8_t* dq, uint8_t* dsf, float* dg,
+                   uint32_t* epoch, uint32_t* ticket, cudaStream_t st);
 // Combine + reduce-scatter: each received token's partial over this rank's
 // experts goes to its owner's all-reduce slot; `add` (this rank's shared
 // expert output for its own T_r tokens) joins the rows this rank owns.

@@ -78,7 +78,7 @@ EpPeers make_ep(const std::vector<int64_t>& bases, int64_t rank, int64_t max_t, 
   p.max_t = max_t;
   p.hidden = hidden;
   p.K = K;
-  ep_layout(p.world, max_t, hidden, K, &p.par_bytes, &p.off_sf, &p.off_ids, &p.off_w);
+  ep_layout(p.world, max_t, hidden, K, &p.par_bytes, &p.off_sf, &p.off_ids, &p.off_w, &p.off_g);
   return p;
 }
 
@@ -88,16 +88,19 @@ int64_t ep_buffer_size(int64_t world, int64_t max_t, int64_t hidden, int64_t K) 
 
 cudaStream_t cur() { return at::cuda::getCurrentCUDAStream().stream(); }
 
-void ep_dispatch(const at::Tensor& q, const at::Tensor& sf, const at::Tensor& ids, const at::Tensor& w, int64_t T_step,
-                 int64_t experts_per_rank, std::vector<int64_t> bases, int64_t rank, int64_t max_t, const at::Tensor& epoch,
-                 at::Tensor ticket) {
-  TORCH_CHECK(q.is_cuda() && q.dim() == 2 && q.is_contiguous(), "q e4m3 [T, hidden]");
+void ep_dispatch(const at::Tensor& q, const at::Tensor& sf, c10::optional<at::Tensor> gs, int64_t hidden,
+                 const at::Tensor& ids, const at::Tensor& w, int64_t T_step, int64_t experts_per_rank,
+                 std::vector<int64_t> bases, int64_t rank, int64_t max_t, const at::Tensor& epoch, at::Tensor ticket) {
+  TORCH_CHECK(q.is_cuda() && q.dim() == 2 && q.is_contiguous(), "q [T, hidden] e4m3 or [T, hidden/2] e2m1 pairs");
   TORCH_CHECK(ids.scalar_type() == at::kInt && ids.is_contiguous() && w.scalar_type() == at::kFloat && w.is_contiguous(),
               "ids int32 / w fp32 [T, K]");
+  const bool fp4 = gs.has_value() && gs->defined();
+  TORCH_CHECK(q.size(1) == (fp4 ? hidden / 2 : hidden), "row bytes");
   const c10::cuda::CUDAGuard g(q.device());
-  EpPeers p = make_ep(bases, rank, max_t, q.size(1), ids.size(1));
+  EpPeers p = make_ep(bases, rank, max_t, hidden, ids.size(1));
   const int rc = b200_ep_dispatch(reinterpret_cast<const uint8_t*>(q.data_ptr()),
-                                  reinterpret_cast<const uint8_t*>(sf.data_ptr()), ids.data_ptr<int>(),
+                                  reinterpret_cast<const uint8_t*>(sf.data_ptr()), optr<float>(gs), fp4 ? 1 : 0,
+                                  ids.data_ptr<int>(),
                                   w.data_ptr<float>(), ids.size(0), T_step, experts_per_rank, &p,
                                   reinterpret_cast<const uint32_t*>(epoch.data_ptr()),
                                   reinterpret_cast<uint32_t*>(ticket.data_ptr()), cur());
@@ -120,11 +123,14 @@ void ep_align(std::vector<int64_t> bases, int64_t rank, int64_t max_t, int64_t h
 }
 
 void ep_gather(std::vector<int64_t> bases, int64_t rank, int64_t max_t, int64_t hidden, int64_t K, int64_t T_step,
-               const at::Tensor& pair_row, at::Tensor dq, at::Tensor dsf, at::Tensor epoch, at::Tensor ticket) {
+               const at::Tensor& pair_row, at::Tensor dq, at::Tensor dsf, c10::optional<at::Tensor> dg,
+               at::Tensor epoch, at::Tensor ticket) {
   const c10::cuda::CUDAGuard g(pair_row.device());
   EpPeers p = make_ep(bases, rank, max_t, hidden, K);
-  const int rc = b200_ep_gather(&p, T_step, pair_row.data_ptr<int>(), reinterpret_cast<uint8_t*>(dq.data_ptr()),
-                                reinterpret_cast<uint8_t*>(dsf.data_ptr()), reinterpret_cast<uint32_t*>(epoch.data_ptr()),
+  const bool fp4 = dg.has_value() && dg->defined();
+  const int rc = b200_ep_gather(&p, T_step, pair_row.data_ptr<int>(), fp4 ? 1 : 0,
+                                reinterpret_cast<uint8_t*>(dq.data_ptr()), reinterpret_cast<uint8_t*>(dsf.data_ptr()),
+                                optr<float>(dg), reinterpret_cast<uint32_t*>(epoch.data_ptr()),
                                 reinterpret_cast<uint32_t*>(ticket.data_ptr()), cur());
   TORCH_CHECK(rc == 0, "ep_gather failed ", rc);
 }

@@ -43,6 +43,7 @@ __device__ __forceinline__ uint8_t* region(const EpPeers& P, int q, int parity) 
 
 __global__ void __launch_bounds__(kThreads) ep_dispatch_kernel(const uint8_t* __restrict__ q,
                                                                 const uint8_t* __restrict__ sf,
+                                                                const float* __restrict__ g, int fp4,
                                                                 const int* __restrict__ ids,
                                                                 const float* __restrict__ w, int T_r, int T_step,
                                                                 int experts_per_rank, EpPeers P, const uint32_t* epoch,
@@ -67,7 +68,8 @@ __global__ void __launch_bounds__(kThreads) ep_dispatch_kernel(const uint8_t* __
   }
   __syncthreads();
   const uint32_t mask = mask_s;
-  const int kb = P.hidden / 32;
+  const int row_bytes = fp4 ? P.hidden / 2 : P.hidden;
+  const int kb = fp4 ? P.hidden / 16 : P.hidden / 32;   // scale columns
   const int words = kb / 4;                 // 4 scale bytes (4 k-blocks) per word
   for (int d = 0; d < P.world; ++d) {
     uint8_t* reg = region(P, d, p);
@@ -78,9 +80,10 @@ __global__ void __launch_bounds__(kThreads) ep_dispatch_kernel(const uint8_t* __
       dw[(int64_t)row * K + k] = valid ? __ldg(w + t * K + k) : 0.f;
     }
     if (!((mask >> d) & 1u)) continue;
-    const uint4* src = reinterpret_cast<const uint4*>(q + (int64_t)t * P.hidden);
-    uint4* dst = reinterpret_cast<uint4*>(reg + (int64_t)row * P.hidden);
-    for (int i = threadIdx.x; i < P.hidden / 16; i += kThreads) dst[i] = __ldg(src + i);
+    const uint4* src = reinterpret_cast<const uint4*>(q + (int64_t)t * row_bytes);
+    uint4* dst = reinterpret_cast<uint4*>(reg + (int64_t)row * row_bytes);
+    for (int i = threadIdx.x; i < row_bytes / 16; i += kThreads) dst[i] = __ldg(src + i);
+    if (fp4 && threadIdx.x == 0) reinterpret_cast<float*>(reg + P.off_g)[row] = __ldg(g + t);
     uint8_t* dsf = reg + P.off_sf;
     for (int c = threadIdx.x; c < words; c += kThreads) {
       const uint32_t v = *reinterpret_cast<const uint32_t*>(sf + moe::sf_offset(t, 4 * c, kb));
@@ -112,8 +115,9 @@ __global__ void __launch_bounds__(1024) ep_align_kernel(EpPeers P, int T_step, i
                       ttile2, sh);
 }
 
-__global__ void __launch_bounds__(kThreads) ep_gather_kernel(EpPeers P, int T_step, const int* pair_row, uint8_t* dq,
-                                                              uint8_t* dsf, uint32_t* epoch, uint32_t* ticket) {
+__global__ void __launch_bounds__(kThreads) ep_gather_kernel(EpPeers P, int T_step, const int* pair_row, int fp4,
+                                                              uint8_t* dq, uint8_t* dsf, float* dg, uint32_t* epoch,
+                                                              uint32_t* ticket) {
   pdl_wait();
   pdl_launch_dependents();
   const int p = (*epoch) & 1;
@@ -121,7 +125,20 @@ __global__ void __launch_bounds__(kThreads) ep_gather_kernel(EpPeers P, int T_st
   uint8_t* mine = P.base[P.rank];
   const uint8_t* reg = region(P, P.rank, p);
   const int r = __ldcg(pair_row + i);
-  if (r >= 0) moe::moe_gather_pair(reg, reg + P.off_sf, i / P.K, r, P.hidden, dq, dsf);
+  if (r >= 0) {
+    const int t = i / P.K;
+    if (fp4) {
+      const int rb = P.hidden / 2, nb = P.hidden / 16;
+      const uint4* s = reinterpret_cast<const uint4*>(reg + (int64_t)t * rb);
+      uint4* d = reinterpret_cast<uint4*>(dq + (int64_t)r * rb);
+      for (int j = threadIdx.x; j < rb / 16; j += blockDim.x) d[j] = __ldcg(s + j);
+      for (int b = threadIdx.x; b < nb; b += blockDim.x)
+        dsf[moe::sf_offset(r, b, nb)] = __ldcg(reg + P.off_sf + moe::sf_offset(t, b, nb));
+      if (threadIdx.x == 0) dg[r] = __ldcg(reinterpret_cast<const float*>(reg + P.off_g) + t);
+    } else {
+      moe::moe_gather_pair(reg, reg + P.off_sf, t, r, P.hidden, dq, dsf);
+    }
+  }
   // completion: the last CTA frees this parity for the dispatch two layers on
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -190,14 +207,14 @@ __global__ void __launch_bounds__(256) ep_combine_rs_kernel(const __nv_bfloat16*
 }  // namespace ep
 }  // namespace b200
 
-int b200_ep_dispatch(const uint8_t* q, const uint8_t* sf, const int* ids, const float* w, int T_r, int T_step,
-                     int experts_per_rank, const EpPeers* peers, const uint32_t* epoch, uint32_t* ticket,
-                     cudaStream_t st) {
+int b200_ep_dispatch(const uint8_t* q, const uint8_t* sf, const float* g, int fp4, const int* ids, const float* w,
+                     int T_r, int T_step, int experts_per_rank, const EpPeers* peers, const uint32_t* epoch,
+                     uint32_t* ticket, cudaStream_t st) {
   if (T_step <= 0 || T_r > T_step || T_step > peers->max_t || peers->world > kArMaxRanks || peers->hidden % 128 ||
-      experts_per_rank <= 0)
+      experts_per_rank <= 0 || (fp4 && !g))
     return -1;
-  b200::launch_pdl(b200::ep::ep_dispatch_kernel, dim3(T_step), dim3(b200::ep::kThreads), 0, st, q, sf, ids, w, T_r,
-                   T_step, experts_per_rank, *peers, epoch, ticket);
+  b200::launch_pdl(b200::ep::ep_dispatch_kernel, dim3(T_step), dim3(b200::ep::kThreads), 0, st, q, sf, g, fp4, ids, w,
+                   T_r, T_step, experts_per_rank, *peers, epoch, ticket);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
 
@@ -211,12 +228,12 @@ int b200_ep_align(const EpPeers* peers, int T_step, int first, int E, int* seg_s
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
 
-int b200_ep_gather(const EpPeers* peers, int T_step, const int* pair_row, uint8_t* dq, uint8_t* dsf, uint32_t* epoch,
-                   uint32_t* ticket, cudaStream_t st) {
-  if (T_step <= 0 || T_step > peers->max_t) return -1;
+int b200_ep_gather(const EpPeers* peers, int T_step, const int* pair_row, int fp4, uint8_t* dq, uint8_t* dsf, float* dg,
+                   uint32_t* epoch, uint32_t* ticket, cudaStream_t st) {
+  if (T_step <= 0 || T_step > peers->max_t || (fp4 && !dg)) return -1;
   const int npairs = peers->world * T_step * peers->K;
   b200::launch_pdl(b200::ep::ep_gather_kernel, dim3(npairs), dim3(b200::ep::kThreads), 0, st, *peers, T_step, pair_row,
-                   dq, dsf, epoch, ticket);
+                   fp4, dq, dsf, dg, epoch, ticket);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
 

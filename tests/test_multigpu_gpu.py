@@ -112,7 +112,7 @@ def _dp_batch(rank, cfg, dev):
     return build_batch(seqs, 64, device=dev)
 
 
-def _dp_rank(rank, world, comm_impl):
+def _dp_rank(rank, world, comm_impl, fmt="mxfp8"):
     import torch
     from b200ds import ops
     from b200ds.config import EngineConfig, small_gpu_config
@@ -121,7 +121,7 @@ def _dp_rank(rank, world, comm_impl):
     from b200ds.parallel.state import ParallelState, init_parallel
     ps = init_parallel(backend="nccl", dp_attention=True, timeout_s=60)
     ops.set_impl("native")
-    cfg = small_gpu_config(num_attention_heads=16)
+    cfg = small_gpu_config(num_attention_heads=16, expert_format=fmt)
     sd = init_weights(cfg, 0)
     ecfg = EngineConfig(tp_size=1, ep_size=world, dp_attention=True, comm_impl=comm_impl)
     m = build_model(cfg, ecfg, ps, sd, device=ps.device)
@@ -139,13 +139,13 @@ def _dp_rank(rank, world, comm_impl):
     return rank, out, ref
 
 
-@pytest.mark.parametrize("comm_impl", ["nccl", "fused"])
-def test_dp2_ep2_matches_single_gpu(comm_impl):
+@pytest.mark.parametrize("comm_impl,fmt", [("nccl", "mxfp8"), ("fused", "mxfp8"), ("fused", "nvfp4")])
+def test_dp2_ep2_matches_single_gpu(comm_impl, fmt):
     """DP attention + EP MoE on 2 GPUs, ranks with different token counts:
     each rank's logits follow a 1-GPU run of its own batch (fp8 noise only).
     The fused path exercises ep_dispatch / ep_align / ep_gather and the
     combine + reduce-scatter into ar_reduce_norm."""
     _needs(2)
-    res = run_ranks(_dp_rank, 2, comm_impl, timeout=600)
+    res = run_ranks(_dp_rank, 2, comm_impl, fmt, timeout=600)
     for rank, out, ref in res:
         assert _rel(out, ref) < 0.15, (rank, _rel(out, ref))
