@@ -16,7 +16,7 @@ import torch
 
 from ..config import EngineConfig, ModelConfig
 from ..ops import ExpertWeights
-from ..ops.quant import MXFP8Tensor, mxfp8_from_block128, quant_mxfp8_ref, pack_sf, sf_packed_size, NVFP4Tensor, quant_nvfp4_ref
+from ..ops.quant import MXFP8Tensor, mxfp8_from_block128, quant_mxfp8_ref, pack_sf, sf_packed_size, NVFP4Tensor, quant_nvfp4_ref, tile_rows128
 from ..parallel.state import ParallelState
 from .deepseek import AttnWeights, DeepseekModel, DenseWeights, LayerWeights, Linear, MoEWeights
 
@@ -50,6 +50,22 @@ def _stack(ws: List[object]) -> object:
         return NVFP4Tensor(torch.stack([w.data for w in ws]), torch.stack([w.sf for w in ws]),
                            torch.stack([w.global_scale.reshape(()) for w in ws]), ws[0].rows)
     return torch.stack(ws)
+
+
+def _maybe_tile(ex: ExpertWeights) -> ExpertWeights:
+    """GPU experts with 64 or fewer per rank are stored as contiguous
+    128 x 128-byte tiles (the grouped GEMM's TMA boxes)."""
+    if ex.count > 64 or not ex.w13.data.is_cuda:
+        return ex
+    for name in ("w13", "w2"):
+        t = getattr(ex, name)
+        d = tile_rows128(t.data.view(torch.uint8)).view(t.data.dtype)
+        if isinstance(t, MXFP8Tensor):
+            setattr(ex, name, MXFP8Tensor(d, t.sf, t.rows))
+        else:
+            setattr(ex, name, NVFP4Tensor(d, t.sf, t.global_scale, t.rows))
+    ex.tiled = True
+    return ex
 
 
 def build_model(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState,
@@ -115,8 +131,8 @@ def build_model(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState,
                 w13.append(_quantize(torch.cat([get(q + "gate_proj.weight"), get(q + "up_proj.weight")], 0),
                                      cfg.expert_format, dev))
                 w2.append(_quantize(get(q + "down_proj.weight"), cfg.expert_format, dev))
-            ex = ExpertWeights(first=first, count=per, w13=_stack(w13), w2=_stack(w2),
-                               inter=cfg.moe_intermediate_size)
+            ex = _maybe_tile(ExpertWeights(first=first, count=per, w13=_stack(w13), w2=_stack(w2),
+                                           inter=cfg.moe_intermediate_size))
             sgu = sdn = None
             if cfg.n_shared_experts:
                 q = m + "shared_experts."

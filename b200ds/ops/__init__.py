@@ -70,6 +70,9 @@ class ExpertWeights:
     # NVFP4 experts: fixed fp32 global scale of the FC2 input (the SwiGLU
     # output), so e4m3 block scales cover block maxima up to 448*6*scale.
     fc2_act_scale: float = 1.0 / 32
+    # weights stored as contiguous 128-row x 128-byte tiles (GPU serving
+    # layout, see ops.quant.tile_rows128)
+    tiled: bool = False
 
 
 @dataclass

@@ -45,6 +45,16 @@ def gemm(a, w: MXFP8Tensor, out_dtype=torch.bfloat16) -> torch.Tensor:
     return (dequant_mxfp8(a.q, a.sf).to(torch.bfloat16) @ dequant_mxfp8(w.data, w.sf).to(torch.bfloat16).t()).to(out_dtype)
 
 
+def _rows(ex, name: str, e: int) -> torch.Tensor:
+    """Expert e's weight as a plain row-major matrix (undoing the tiled
+    serving layout when the experts use it)."""
+    d = getattr(ex, name).data[e]
+    if getattr(ex, "tiled", False):
+        from .quant import untile_rows128
+        d = untile_rows128(d.view(torch.uint8)).view(d.dtype)
+    return d
+
+
 def moe_experts(a, w, ids, ex, out_dtype=torch.bfloat16):
     """Per-expert loop over library GEMMs (host-synchronising)."""
     T = a.q.shape[0]
@@ -61,9 +71,10 @@ def moe_experts(a, w, ids, ex, out_dtype=torch.bfloat16):
         xe = _qact(a.q[tok_d], None)
         xf = dequant_mxfp8(a.q, a.sf)[tok_d]
         xe = quant(xf)
-        y = gemm(xe, MXFP8Tensor(ex.w13.data[e], ex.w13.sf[e]), torch.float32)
+        w13, w2 = _rows(ex, "w13", e), _rows(ex, "w2", e)
+        y = gemm(xe, MXFP8Tensor(w13, ex.w13.sf[e]), torch.float32)
         I = y.shape[1] // 2
         h = torch.nn.functional.silu(y[:, :I]) * y[:, I:]
-        o = gemm(quant(h), MXFP8Tensor(ex.w2.data[e], ex.w2.sf[e]), torch.float32)
+        o = gemm(quant(h), MXFP8Tensor(w2, ex.w2.sf[e]), torch.float32)
         out.index_add_(0, tok_d, we * o)
     return out.to(out_dtype)

@@ -280,10 +280,10 @@ def moe_experts(h, w: torch.Tensor, ids: torch.Tensor, ex, out_dtype=torch.bfloa
     hq = alloc_qact(max_rows, I, dev)
     w13, w2 = ex.w13, ex.w2
     _C.gemm_grouped(w13.data, w13.sf, xs.q, xs.sf, 2 * I, Hd, E, I, bn1, seg_start, seg_count, tt1, 2,
-                    None, 0, hq.q, hq.sf, I, None, 0, True)
+                    None, 0, hq.q, hq.sf, I, None, 0, True, a_tiled=ex.tiled)
     y = torch.empty(max_rows, Hd, dtype=torch.bfloat16, device=dev)
     _C.gemm_grouped(w2.data, w2.sf, hq.q, hq.sf, Hd, I, E, 0, bn2, seg_start, seg_count, tt2, 3,
-                    y, Hd, None, None, 0, row_weight, 0, True)
+                    y, Hd, None, None, 0, row_weight, 0, True, a_tiled=ex.tiled)
     if not combine:
         from . import MoEPartial
         return MoEPartial(y, pair_row, None)
@@ -344,10 +344,10 @@ def moe_experts_nvfp4(h, w, ids, ex, out_dtype=torch.bfloat16, n_experts_total=N
     w13, w2 = ex.w13, ex.w2
     g2 = float(ex.fc2_act_scale)
     _C.gemm_grouped(w13.data, w13.sf, xs_q, xs_sf, 2 * I, Hd, E, I, bn1, seg_start, seg_count, tt1, 2,
-                    None, 0, hq, hsf, I, None, 0, True, w_g=w13.global_scale, x_g=xs_g, out_g=g2)
+                    None, 0, hq, hsf, I, None, 0, True, w_g=w13.global_scale, x_g=xs_g, out_g=g2, a_tiled=ex.tiled)
     y = torch.empty(max_rows, Hd, dtype=torch.bfloat16, device=dev)
     _C.gemm_grouped(w2.data, w2.sf, hq, hsf, Hd, I, E, 0, bn2, seg_start, seg_count, tt2, 3,
-                    y, Hd, None, None, 0, row_weight, 0, True, w_g=w2.global_scale, x_g_const=g2)
+                    y, Hd, None, None, 0, row_weight, 0, True, w_g=w2.global_scale, x_g_const=g2, a_tiled=ex.tiled)
     if not combine:
         from . import MoEPartial
         return MoEPartial(y, pair_row, None)
@@ -406,18 +406,18 @@ def moe_experts_ep(h, w, ids, ex, T_step: int, n_experts_total: int, ep):
         hsf = torch.empty(max_rows * (I // 16), dtype=torch.uint8, device=dev)
         g2 = float(ex.fc2_act_scale)
         _C.gemm_grouped(w13.data, w13.sf, xs_q, xs_sf, 2 * I, Hd, E, I, bn1, seg_start, seg_count, tt1, 2,
-                        None, 0, hq, hsf, I, None, 0, True, w_g=w13.global_scale, x_g=xs_g, out_g=g2)
+                        None, 0, hq, hsf, I, None, 0, True, w_g=w13.global_scale, x_g=xs_g, out_g=g2, a_tiled=ex.tiled)
         _C.gemm_grouped(w2.data, w2.sf, hq, hsf, Hd, I, E, 0, bn2, seg_start, seg_count, tt2, 3,
-                        y, Hd, None, None, 0, row_weight, 0, True, w_g=w2.global_scale, x_g_const=g2)
+                        y, Hd, None, None, 0, row_weight, 0, True, w_g=w2.global_scale, x_g_const=g2, a_tiled=ex.tiled)
         return EPPartial(y, pair_row, T_step, T_r)
     xs = alloc_qact(max_rows, Hd, dev)
     _C.ep_gather(ep.bases, ep.rank, ep.max_t, Hd, K, T_step, pair_row, xs.q, xs.sf, None, ep.epoch,
                  ep.gather_ticket)
     hq = alloc_qact(max_rows, I, dev)
     _C.gemm_grouped(w13.data, w13.sf, xs.q, xs.sf, 2 * I, Hd, E, I, bn1, seg_start, seg_count, tt1, 2,
-                    None, 0, hq.q, hq.sf, I, None, 0, True)
+                    None, 0, hq.q, hq.sf, I, None, 0, True, a_tiled=ex.tiled)
     _C.gemm_grouped(w2.data, w2.sf, hq.q, hq.sf, Hd, I, E, 0, bn2, seg_start, seg_count, tt2, 3,
-                    y, Hd, None, None, 0, row_weight, 0, True)
+                    y, Hd, None, None, 0, row_weight, 0, True, a_tiled=ex.tiled)
     return EPPartial(y, pair_row, T_step, T_r)
 
 

@@ -79,6 +79,22 @@ def unpack_sf(packed: torch.Tensor, rows: int, k: int) -> torch.Tensor:
     return t.view(Rp, KB)[:rows]
 
 
+def tile_rows128(data: torch.Tensor) -> torch.Tensor:
+    """[..., R, C] bytes (R, C multiples of 128) -> the same bytes stored as
+    contiguous 128-row x 128-byte tiles, tile order (row block, column block),
+    returned with the original shape.  The grouped GEMM reads such weights
+    with one contiguous 16 KB block per TMA box."""
+    *lead, R, C = data.shape
+    t = data.reshape(*lead, R // 128, 128, C // 128, 128).transpose(-3, -2).contiguous()
+    return t.reshape(*lead, R, C)
+
+
+def untile_rows128(data: torch.Tensor) -> torch.Tensor:
+    *lead, R, C = data.shape
+    t = data.reshape(*lead, R // 128, C // 128, 128, 128).transpose(-3, -2).contiguous()
+    return t.reshape(*lead, R, C)
+
+
 # ---------------------------------------------------------------------------
 # MXFP8 tensors
 # ---------------------------------------------------------------------------

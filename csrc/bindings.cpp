@@ -204,7 +204,7 @@ void gemm_grouped(const at::Tensor& w, const at::Tensor& w_sf, const at::Tensor&
                   const at::Tensor& seg_count, const at::Tensor& ttile_off, int64_t epi, c10::optional<at::Tensor> out,
                   int64_t ldo, c10::optional<at::Tensor> q_out, c10::optional<at::Tensor> sf_out, int64_t ldq,
                   c10::optional<at::Tensor> row_weight, int64_t num_ctas, bool pdl, c10::optional<at::Tensor> w_g,
-                  c10::optional<at::Tensor> x_g, double x_g_const, double out_g) {
+                  c10::optional<at::Tensor> x_g, double x_g_const, double out_g, bool a_tiled) {
   check_cuda(w, "w");
   const c10::cuda::CUDAGuard g(w.device());
   TORCH_CHECK(k % 128 == 0 && nw % 128 == 0, "k and nw must be multiples of 128");
@@ -237,6 +237,7 @@ void gemm_grouped(const at::Tensor& w, const at::Tensor& w_sf, const at::Tensor&
   a.x_g = optr<float>(x_g);
   a.x_g_const = float(x_g_const);
   a.out_g = float(out_g);
+  a.a_tiled = a_tiled ? 1 : 0;
   check(b200_gemm_grouped(&a, cur_stream()), "gemm_grouped");
 }
 
@@ -321,7 +322,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine", &moe_combine);
   m.def("gemm_grouped", &gemm_grouped, pybind11::arg("w"), pybind11::arg("w_sf"), pybind11::arg("x"), pybind11::arg("x_sf"), pybind11::arg("nw"), pybind11::arg("k"), pybind11::arg("E"), pybind11::arg("inter"), pybind11::arg("bn"), pybind11::arg("seg_start"), pybind11::arg("seg_count"), pybind11::arg("ttile_off"), pybind11::arg("epi"), pybind11::arg("out"), pybind11::arg("ldo"), pybind11::arg("q_out"), pybind11::arg("sf_out"), pybind11::arg("ldq"), pybind11::arg("row_weight"), pybind11::arg("num_ctas"), pybind11::arg("pdl"),
         pybind11::arg("w_g") = pybind11::none(), pybind11::arg("x_g") = pybind11::none(),
-        pybind11::arg("x_g_const") = 1.0, pybind11::arg("out_g") = 1.0);
+        pybind11::arg("x_g_const") = 1.0, pybind11::arg("out_g") = 1.0, pybind11::arg("a_tiled") = false);
   m.def("nvfp4_quant", &nvfp4_quant);
   m.def("moe_gather4", &moe_gather4);
   m.def("num_sms", &num_sms);

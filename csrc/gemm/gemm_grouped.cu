@@ -81,6 +81,7 @@ struct Params {
   const float* x_g;          // NVFP4: per-row activation global scale (or null)
   float x_g_const;
   float out_g;               // NVFP4 FC1: global scale of the requantized output
+  int a_tiled;               // weights stored as contiguous 128 x 128-byte tiles (3-D tensor map)
 };
 
 __device__ __forceinline__ int64_t sf_offset(int row, int kblock, int kb_total) {
@@ -93,6 +94,7 @@ struct Tile {
   int e, tile_n, tt, rows;
 };
 
+
 // Tiles are ordered (expert, token tile) major, output-row tile minor, so
 // CTAs running at the same time share the expert's activation rows in L2.
 // The routing layout (tile offsets, segment starts / counts) is staged in
@@ -100,8 +102,8 @@ struct Tile {
 // seg_start, [2E+1..3E] = seg_count.
 constexpr int kMaxExperts = 256;
 __device__ __forceinline__ Tile map_tile(const Params& p, const int* lay, int w) {
-  const int ttg = w / p.n_tiles;
   Tile t;
+  const int ttg = w / p.n_tiles;
   t.tile_n = w - ttg * p.n_tiles;
   int lo = 0, hi = p.E;   // e with ttile_off[e] <= ttg < ttile_off[e+1]
   while (hi - lo > 1) {
@@ -190,9 +192,17 @@ grouped_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
           if (it >= C::kStages && !mbar_wait(&empty[s], ((it / C::kStages) - 1) & 1, p.err)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[s], bytes);
           uint8_t* a_dst = sA + (size_t)s * C::kA * kTileM * kTileK;
-          tma_load_2d_hint(a_dst, &tm_a, &full[s], kt * kTileK, a_row, pol_w);
-          if (EPI == kEpiSwiglu)
-            tma_load_2d_hint(a_dst + kTileM * kTileK, &tm_a, &full[s], kt * kTileK, a_row + p.inter, pol_w);
+          if (p.a_tiled) {
+            // tile (row block, k-tile) = one contiguous 16 KB block
+            tma_load_3d_hint(a_dst, &tm_a, &full[s], 0, 0, (a_row >> 7) * nk + kt, pol_w);
+            if (EPI == kEpiSwiglu)
+              tma_load_3d_hint(a_dst + kTileM * kTileK, &tm_a, &full[s], 0, 0, ((a_row + p.inter) >> 7) * nk + kt,
+                               pol_w);
+          } else {
+            tma_load_2d_hint(a_dst, &tm_a, &full[s], kt * kTileK, a_row, pol_w);
+            if (EPI == kEpiSwiglu)
+              tma_load_2d_hint(a_dst + kTileM * kTileK, &tm_a, &full[s], kt * kTileK, a_row + p.inter, pol_w);
+          }
           tma_load_2d_hint(sB + (size_t)s * BN * kTileK, &tm_b, &full[s], kt * kTileK, b_row, pol_x);
           uint8_t* sfa_dst = sSFA + (size_t)s * C::kA * C::kSfK;
           const int kc0 = kt * kChunksPerTile;
@@ -378,7 +388,7 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-static int map_u8(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows) {
+static EncodeTiledFn encoder() {
   static EncodeTiledFn enc = nullptr;
   if (!enc) {
     cudaDriverEntryPointQueryResult q;
@@ -386,6 +396,25 @@ static int map_u8(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, 
     cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
     enc = reinterpret_cast<EncodeTiledFn>(ptr);
   }
+  return enc;
+}
+
+// Tiled weights: [blocks][128 rows][128 bytes] with blocks = rows/128 * cols/128.
+static int map_u8_tiled(CUtensorMap* m, const void* base, int64_t rows, int64_t cols) {
+  EncodeTiledFn enc = encoder();
+  if (!enc) return -1;
+  cuuint64_t dims[3] = {128u, 128u, (cuuint64_t)((rows / 128) * (cols / 128))};
+  cuuint64_t strides[2] = {128u, 128u * 128u};
+  cuuint32_t box[3] = {128u, 128u, 1u};
+  cuuint32_t es[3] = {1u, 1u, 1u};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : int(r);
+}
+
+static int map_u8(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows) {
+  EncodeTiledFn enc = encoder();
   if (!enc) return -1;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)cols};
@@ -402,7 +431,9 @@ static int launch(const GroupedArgs& a, cudaStream_t st) {
   using C = Cfg<BN, EPI, FP4>;
   CUtensorMap ma, mb;
   const int kbytes = FP4 ? a.k / 2 : a.k;
-  if (map_u8(&ma, a.w, (int64_t)a.E * a.nw, kbytes, kTileM)) return -2;
+  if (a.a_tiled ? map_u8_tiled(&ma, a.w, (int64_t)a.E * a.nw, kbytes)
+                : map_u8(&ma, a.w, (int64_t)a.E * a.nw, kbytes, kTileM))
+    return -2;
   if (map_u8(&mb, a.x, a.x_rows, kbytes, BN)) return -3;
   Params p{};
   p.sfa = a.w_sf;
@@ -427,6 +458,7 @@ static int launch(const GroupedArgs& a, cudaStream_t st) {
   p.x_g = a.x_g;
   p.x_g_const = a.x_g_const;
   p.out_g = a.out_g;
+  p.a_tiled = a.a_tiled;
   auto kern = grouped_kernel<BN, EPI, FP4>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
   cudaLaunchConfig_t cfg = {};

@@ -77,6 +77,11 @@ struct GroupedArgs {
   // in the same 128-row x 4-column chunk layout; fp32 global scales: w_g per
   // expert, x_g per sorted activation row (or x_g_const when null); FC1
   // writes its SwiGLU output as NVFP4 with global scale out_g.
+  // a_tiled = 1: w is stored as contiguous 128-row x 128-byte tiles,
+  // [E * nw / 128][k_bytes / 128][128][128], so every TMA box reads one
+  // contiguous 16 KB block (short weight rows otherwise scatter each box
+  // over 128 DRAM rows).
+  int a_tiled;
   int fp4;
   const float* w_g;
   const float* x_g;

@@ -466,3 +466,32 @@ def test_moe_experts_nvfp4(T):
     exc = ExpertWeights(8, E, cpu(ex.w13), cpu(ex.w2), I)
     exp = ops.moe_experts(x.float().cpu(), wts.cpu(), ids.cpu(), exc, torch.float32)
     assert rel_err(got.cpu(), exp) < 5e-2, rel_err(got.cpu(), exp)
+
+
+@pytest.mark.parametrize("fp4", [False, True])
+def test_grouped_tiled_weights_identical(fp4):
+    """Weights stored as contiguous 128 x 128-byte tiles (3-D TMA map) give
+    bit-identical grouped-GEMM results."""
+    from b200ds.ops import ExpertWeights, cuda
+    from b200ds.ops.quant import MXFP8Tensor, NVFP4Tensor, tile_rows128, untile_rows128
+    T, H, I, E, K = 40, 1024, 256, 8, 4
+    torch.manual_seed(0)
+    if fp4:
+        w13, w2 = _nvfp4_stack(E, 2 * I, H), _nvfp4_stack(E, H, I)
+        tile = lambda t: NVFP4Tensor(tile_rows128(t.data), t.sf, t.global_scale, t.rows)
+    else:
+        mk = lambda N, Kd: [_mx(torch.randn(N, Kd, device=DEV) * 0.05) for _ in range(E)]
+        a13, a2 = mk(2 * I, H), mk(H, I)
+        w13 = MXFP8Tensor(torch.stack([w.data for w in a13]), torch.stack([w.sf for w in a13]))
+        w2 = MXFP8Tensor(torch.stack([w.data for w in a2]), torch.stack([w.sf for w in a2]))
+        tile = lambda t: MXFP8Tensor(tile_rows128(t.data.view(torch.uint8)).view(t.data.dtype), t.sf, t.rows)
+    assert torch.equal(untile_rows128(tile_rows128(w2.data.view(torch.uint8))), w2.data.view(torch.uint8))
+    ex = ExpertWeights(0, E, w13, w2, I)
+    ext = ExpertWeights(0, E, tile(w13), tile(w2), I)
+    ext.tiled = True
+    x = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    ids = torch.stack([torch.randperm(E, device=DEV)[:K] for _ in range(T)]).int()
+    wts = torch.rand(T, K, device=DEV)
+    f = cuda.moe_experts_nvfp4 if fp4 else (lambda *a: cuda.moe_experts(cuda.quant(a[0]), *a[1:]))
+    a, b = f(x, wts, ids, ex, torch.float32), f(x, wts, ids, ext, torch.float32)
+    assert torch.equal(a, b)
