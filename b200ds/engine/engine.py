@@ -163,6 +163,7 @@ class Engine:
         else:
             toks = self._forward(st)
         self.sched.commit(st)
+        self._check_device_errors()
         now = time.perf_counter()
         done = []
         self.stats["steps"] += 1
@@ -187,6 +188,14 @@ class Engine:
                 self.sched.finish(r)
                 done.append(r)
         return done
+
+    def _check_device_errors(self) -> None:
+        """Every device-side wait in the fused collectives is bounded; a wait
+        that ran out (a peer that stopped pushing) leaves an error word on
+        the device instead of hanging the GPU.  Surface it after each step."""
+        for obj in (getattr(self.ps, "fused_ar", None), getattr(self.ps, "fused_ep", None)):
+            if obj is not None:
+                obj.check()
 
     def generate(self, prompts: Sequence[Union[str, Sequence[int]]],
                  params: Union[SamplingParams, Sequence[SamplingParams], None] = None) -> List[GenerateOutput]:

@@ -177,10 +177,10 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
         for (int q = 0; q < kTile / 32; ++q) {
           const int r = q * 32 + lane;                       // row of the tile
           const int j = tok0 + r;                            // list entry
-          const int pos = j < k_hi ? __ldg(list + j) : -1;
+          const int pos = j < k_hi ? __ldcg(list + j) : -1;
           const bool ok = pos >= 0 && pos < n;
           int64_t slot = 0;
-          if (ok) slot = (int64_t)__ldg(p.block_table + (int64_t)b * p.bt_stride + pos / kPage) * kPage + pos % kPage;
+          if (ok) slot = (int64_t)__ldcg(p.block_table + (int64_t)b * p.bt_stride + pos / kPage) * kPage + pos % kPage;
           const uint8_t* src = p.cache + slot * kD;
           const uint32_t nb = ok ? 16u : 0u;
 #pragma unroll
@@ -295,7 +295,7 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
           tmem_ld_wait();
           bool valid = tok0 + row < k_hi;
           if (SPARSE && valid) {
-            const int pos = __ldg(p.topk + (int64_t)t * p.topk_n + tok0 + row);
+            const int pos = __ldcg(p.topk + (int64_t)t * p.topk_n + tok0 + row);
             valid = pos >= 0 && pos < n;
           }
 #pragma unroll

@@ -59,7 +59,7 @@ __global__ void __launch_bounds__(kThreads) ep_dispatch_kernel(const uint8_t* __
   if (threadIdx.x < 32) {
     uint32_t m = 0;
     for (int k = threadIdx.x; k < K; k += 32) {
-      const int id = valid ? __ldg(ids + t * K + k) : -1;
+      const int id = valid ? __ldcg(ids + t * K + k) : -1;
       if (id >= 0) m |= 1u << (id / experts_per_rank);
     }
 #pragma unroll
@@ -76,14 +76,14 @@ __global__ void __launch_bounds__(kThreads) ep_dispatch_kernel(const uint8_t* __
     int* did = reinterpret_cast<int*>(reg + P.off_ids);
     float* dw = reinterpret_cast<float*>(reg + P.off_w);
     for (int k = threadIdx.x; k < K; k += kThreads) {
-      did[(int64_t)row * K + k] = valid ? __ldg(ids + t * K + k) : -1;
-      dw[(int64_t)row * K + k] = valid ? __ldg(w + t * K + k) : 0.f;
+      did[(int64_t)row * K + k] = valid ? __ldcg(ids + t * K + k) : -1;
+      dw[(int64_t)row * K + k] = valid ? __ldcg(w + t * K + k) : 0.f;
     }
     if (!((mask >> d) & 1u)) continue;
     const uint4* src = reinterpret_cast<const uint4*>(q + (int64_t)t * row_bytes);
     uint4* dst = reinterpret_cast<uint4*>(reg + (int64_t)row * row_bytes);
-    for (int i = threadIdx.x; i < row_bytes / 16; i += kThreads) dst[i] = __ldg(src + i);
-    if (fp4 && threadIdx.x == 0) reinterpret_cast<float*>(reg + P.off_g)[row] = __ldg(g + t);
+    for (int i = threadIdx.x; i < row_bytes / 16; i += kThreads) dst[i] = __ldcg(src + i);
+    if (fp4 && threadIdx.x == 0) reinterpret_cast<float*>(reg + P.off_g)[row] = __ldcg(g + t);
     uint8_t* dsf = reg + P.off_sf;
     for (int c = threadIdx.x; c < words; c += kThreads) {
       const uint32_t v = *reinterpret_cast<const uint32_t*>(sf + moe::sf_offset(t, 4 * c, kb));

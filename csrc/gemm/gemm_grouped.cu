@@ -299,7 +299,7 @@ grouped_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
       const int tmax = t.rows - t.tt * BN;
       const int wrow = t.tile_n * kTileM + sub * 32 + lane;
       const uint32_t lane_addr = tmem + buf * C::kAcc + (uint32_t(sub * 32) << 16);
-      const float wg = FP4 ? __ldg(p.w_g + t.e) : 1.f;
+      const float wg = FP4 ? __ldcg(p.w_g + t.e) : 1.f;
       if constexpr (FP4 && EPI == kEpiSwiglu) {
         // h = silu(g) * u with both scaled by the global scales; NVFP4 out:
         // one 16-channel block per half-warp, two channels per byte.

@@ -495,3 +495,30 @@ def test_grouped_tiled_weights_identical(fp4):
     f = cuda.moe_experts_nvfp4 if fp4 else (lambda *a: cuda.moe_experts(cuda.quant(a[0]), *a[1:]))
     a, b = f(x, wts, ids, ex, torch.float32), f(x, wts, ids, ext, torch.float32)
     assert torch.equal(a, b)
+
+
+def test_bounded_wait_reports_timeout():
+    """A device wait on arrivals that never come (a flag nothing sets) gives
+    up after its deadline, writes the error word, leaves a well-formed empty
+    routing layout, and the context stays usable."""
+    import time
+    from b200ds import _C
+    world, max_t, H, K, T_step, E = 1, 16, 1024, 4, 8, 8
+    buf = torch.zeros(int(_C.ep_buffer_size(world, max_t, H, K)), dtype=torch.uint8, device=DEV)
+    epoch = torch.zeros(1, dtype=torch.int32, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    i32 = lambda n: torch.full((n,), 7, dtype=torch.int32, device=DEV)
+    seg_start, seg_count, tt1, tt2, total = i32(E), i32(E), i32(E + 1), i32(E + 1), i32(1)
+    row_token = i32(1024)
+    row_weight = torch.zeros(1024, device=DEV)
+    pair_row = torch.zeros(T_step * world, K, dtype=torch.int32, device=DEV)
+    t0 = time.time()
+    _C.ep_align([buf.data_ptr()], 0, max_t, H, K, T_step, 0, E, seg_start, seg_count, row_token, row_weight,
+                pair_row, total, 16, tt1, 16, tt2, epoch, err)
+    torch.cuda.synchronize()
+    waited = time.time() - t0
+    assert int(err.item()) == 2, int(err.item())           # kErrPeerTimeout
+    assert 1.0 < waited < 30.0, waited
+    assert (pair_row == -1).all() and int(total.item()) == 0 and int(seg_count.sum().item()) == 0
+    x = torch.randn(1000, device=DEV)
+    assert torch.allclose((x * 2).sum(), x.sum() * 2, rtol=1e-4)
