@@ -66,6 +66,12 @@ class DecodeGraphRunner:
         g.h_lens = torch.ones(bs, dtype=torch.int32).pin_memory()
         g.h_bt = torch.zeros(bs, self.max_pages, dtype=torch.int32).pin_memory()
         g.h_tok = torch.zeros(bs, dtype=torch.int64).pin_memory()
+        # per-row sampling parameters (padding rows: greedy)
+        g.samp = torch.zeros(4, bs, dtype=torch.float32, device=d)     # temperature, top_p, top_k, uniform
+        g.samp[1].fill_(1.0)
+        g.temp, g.top_p, g.unif = g.samp[0], g.samp[1], g.samp[3]
+        g.top_k = torch.zeros(bs, dtype=torch.int32, device=d)
+        g.h_samp = torch.zeros(4, bs, dtype=torch.float32).pin_memory()
         g.fb = ForwardBatch(input_ids=g.ids, positions=g.pos, q_seq=g.q_seq, out_slots=g.slots, seq_lens=g.lens,
                             block_table=g.bt, last_idx=g.last, is_decode=True, max_q_len=1,
                             max_seq_len=self.max_pages * self.page_size, dp_tmax=bs)
@@ -77,8 +83,7 @@ class DecodeGraphRunner:
         s.wait_stream(torch.cuda.current_stream(self.dev))
         with torch.cuda.stream(s):
             for _ in range(2):
-                logits = self.model.forward(g.fb)
-                torch.argmax(logits, -1)
+                self.model.forward_tokens(g.fb, g.temp, g.top_p, g.top_k, g.unif)
         torch.cuda.current_stream(self.dev).wait_stream(s)
         torch.cuda.synchronize(self.dev)
         # keep_graph: the raw graph stays queryable (kernel-node census)
@@ -86,8 +91,7 @@ class DecodeGraphRunner:
         if self.pool is None:
             self.pool = torch.cuda.graph_pool_handle()
         with torch.cuda.graph(g.graph, pool=self.pool):
-            g.logits = self.model.forward(g.fb)
-            g.tokens = torch.argmax(g.logits, -1)
+            g.tokens = self.model.forward_tokens(g.fb, g.temp, g.top_p, g.top_k, g.unif)
         g.graph.instantiate()
         self.graphs[bs] = g
         return g
@@ -124,22 +128,38 @@ class DecodeGraphRunner:
         g.lens.copy_(g.h_lens, non_blocking=True)
         g.bt.copy_(g.h_bt, non_blocking=True)
 
+    def stage_sampling(self, g: _Graph, step) -> None:
+        """Per-row temperature / top-p / top-k / uniform for this step."""
+        h = g.h_samp.numpy()
+        h[0].fill(0.0)
+        h[1].fill(1.0)
+        h[2].fill(0.0)
+        h[3].fill(0.0)
+        if step is not None:
+            for i, (r, smp) in enumerate(zip(step.reqs, step.sample)):
+                p = r.params
+                h[0, i] = p.temperature
+                h[1, i] = p.top_p
+                h[2, i] = p.top_k
+                h[3, i] = r.uniform() if (smp and p.temperature > 0) else 0.0
+        g.samp.copy_(g.h_samp, non_blocking=True)
+        g.top_k.copy_(g.samp[2])
+
     def run(self, step, seqs: List[dict], bucket: Optional[int] = None) -> Optional[List[int]]:
         """Replay the graph of `bucket` (default: the smallest that fits);
-        `step` None replays with padding rows only (an idle DP rank)."""
+        `step` None replays with padding rows only (an idle DP rank).  The
+        graph samples on the device; only the token ids come back."""
         n = len(seqs)
         bs = bucket or self._bucket(n)
         g = self.graphs.get(bs) or self.capture(bs)
         self.stage(g, seqs)
+        self.stage_sampling(g, step)
         g.graph.replay()
         if step is None:
             return None
-        greedy = all(r.params.temperature <= 0 for r in step.reqs)
-        if greedy:
-            g.h_tok.copy_(g.tokens, non_blocking=True)
-            torch.cuda.current_stream(self.dev).synchronize()
-            return g.h_tok[:n].tolist()
-        return self.eng._sample(step, g.logits[:n])
+        g.h_tok.copy_(g.tokens, non_blocking=True)
+        torch.cuda.current_stream(self.dev).synchronize()
+        return g.h_tok[:n].tolist()
 
     def release(self) -> None:
         """Drop the graphs (before destroying the process group)."""

@@ -286,6 +286,11 @@ class DeepseekModel:
     @torch.no_grad()
     def forward(self, fb: ForwardBatch) -> torch.Tensor:
         """Returns logits [B, V] (full vocab) for each sequence's last token."""
+        h = self._hidden(fb)
+        return ops.lm_head_logits(self._last_hidden(h, fb), self.lm_head, self.ps)
+
+    def _hidden(self, fb: ForwardBatch):
+        """All decoder layers + the final norm; returns the normed hidden."""
         c = self.cfg
         residual = self.embed[fb.input_ids.long()].float()      # fp32 residual stream
         h = ops.rmsnorm_act(residual, self.layers[0].in_ln, c.rms_norm_eps, self.layers[0].attn.qkv_a)
@@ -301,8 +306,28 @@ class DeepseekModel:
             h, residual = ops.allreduce_add_rmsnorm(
                 f, residual, nxt.in_ln if nxt else self.final_ln, c.rms_norm_eps, ps_f,
                 "ffn", nxt.attn.qkv_a if nxt else None)
-        last = ops.to_float(h)[fb.last_idx] if not isinstance(h, torch.Tensor) or h.dim() == 2 else h[fb.last_idx]
-        return ops.lm_head_logits(last, self.lm_head, self.ps)
+        return h
+
+    def _last_hidden(self, h, fb: ForwardBatch) -> torch.Tensor:
+        x = ops.to_float(h)
+        if x.is_cuda:
+            x = x.to(torch.bfloat16)
+        if fb.is_decode and int(fb.last_idx.shape[0]) == int(x.shape[0]):
+            return x                 # decode: every token is its sequence's last
+        return x[fb.last_idx]
+
+    def vocab_offset(self) -> int:
+        rows = getattr(self.lm_head, "rows", None)
+        n = rows if rows is not None else self.lm_head.shape[0]
+        return self.ps.tp_rank * n
+
+    @torch.no_grad()
+    def forward_tokens(self, fb: ForwardBatch, temperature, top_p, top_k, uniform) -> torch.Tensor:
+        """Forward + sampling without materialising the full-vocabulary
+        logits: returns token ids [B] (greedy for rows with temperature <= 0)."""
+        h = self._hidden(fb)
+        local = ops.lm_head_local(self._last_hidden(h, fb), self.lm_head)
+        return ops.sample_tokens(local, self.vocab_offset(), temperature, top_p, top_k, uniform, self.ps)
 
     def _ffn_first_linear(self, lw: LayerWeights):
         if isinstance(lw.ffn, DenseWeights):

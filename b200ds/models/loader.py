@@ -154,7 +154,9 @@ def build_model(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState,
     emb_dt = torch.bfloat16 if dev.type == "cuda" else torch.float32
     embed = sd["model.embed_tokens.weight"].float().to(dev, emb_dt)
     head_full = sd["model.embed_tokens.weight"] if cfg.tie_word_embeddings else sd["lm_head.weight"]
-    head = split(head_full.float(), 0, tp, tr).to(dev, emb_dt)
+    head = split(head_full.float(), 0, tp, tr)
+    # quantized formats serve the LM head in MXFP8 as well (tcgen05 GEMM)
+    head = _quantize(head, "mxfp8", dev) if fmt_d == "mxfp8" and dev.type == "cuda" else head.to(dev, emb_dt)
     if kv_dtype is None:
         kv_dtype = torch.float8_e4m3fn if dev.type == "cuda" else torch.float32
     return DeepseekModel(cfg, ecfg, ps, layers, embed, sd["model.norm.weight"].float().to(dev), head, dev,

@@ -136,7 +136,9 @@ def build_random_model(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState, 
             dense_list.append(DenseWeights(gate_up=Linear(_gate_up(I, h, dev, sd)), down=Linear(rand_mx((), h, I, dev, sd))))
             shared_list.append((None, None))
     embed = rand_bf16((cfg.vocab_size, h), dev, gen)
-    head = rand_bf16((cfg.vocab_size // tp if cfg.vocab_size % tp == 0 else -(-cfg.vocab_size // tp), h), dev, gen)
+    v_local = cfg.vocab_size // tp if cfg.vocab_size % tp == 0 else -(-cfg.vocab_size // tp)
+    # MXFP8 LM head (vocab-parallel): the tcgen05 GEMM streams half the bytes of bf16
+    head = rand_mx((), v_local, h, dev, sd)
 
     # routed experts: distinct sets as memory allows
     per = cfg.n_routed_experts // ps.ep_size

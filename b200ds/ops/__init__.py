@@ -393,12 +393,32 @@ def _moe_nvfp4_ref(xf: torch.Tensor, w: torch.Tensor, ids: torch.Tensor, ex: Exp
 # LM head / sampling
 # ---------------------------------------------------------------------------
 
-def lm_head_logits(x: torch.Tensor, head: torch.Tensor, ps) -> torch.Tensor:
-    if x.is_cuda:
-        logits = (x.to(head.dtype) @ head.T).float()
-    else:
-        logits = x.float() @ head.float().T
-    return ps.tp_all_gather(logits, dim=-1)
+def lm_head_local(x, head) -> torch.Tensor:
+    """This rank's vocabulary shard of the logits [B, V_local] (bf16 from
+    the MXFP8 tensor-core GEMM for a quantized head, else fp32)."""
+    if isinstance(head, MXFP8Tensor):
+        y = linear(x if isinstance(x, QAct) else to_float(x), head, torch.bfloat16)
+        n = head.rows if head.rows is not None else head.data.shape[0]
+        return y if y.shape[-1] == n else y[..., :n]
+    xf = to_float(x)
+    if xf.is_cuda:
+        return (xf.to(head.dtype) @ head.T).float()
+    return xf.float() @ head.float().T
+
+
+def lm_head_logits(x, head, ps) -> torch.Tensor:
+    """Full-vocabulary fp32 logits (vocab shards all-gathered over TP)."""
+    return ps.tp_all_gather(lm_head_local(x, head).float().contiguous(), dim=-1)
+
+
+def sample_tokens(local_logits: torch.Tensor, vocab_off: int, temperature, top_p, top_k, uniform, ps) -> torch.Tensor:
+    """Token ids [B] sampled from the vocab-parallel logits without gathering
+    them: native kernels exchange per-rank candidates only; the reference
+    path gathers and samples the full logits."""
+    if _use_native(local_logits):
+        return _native().sample_tokens(local_logits, vocab_off, temperature, top_p, top_k, uniform, ps)
+    full = ps.tp_all_gather(local_logits.float().contiguous(), dim=-1)
+    return sample(full, temperature, top_p, top_k, uniform)
 
 
 def sample(logits: torch.Tensor, temperature, top_p, top_k, uniform) -> torch.Tensor:

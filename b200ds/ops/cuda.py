@@ -460,6 +460,42 @@ def indexer_topk(q_raw, w_raw, w_factor, table, k_cache, k_scale, fb, page_size,
     return out
 
 
+SAMPLE_CANDIDATES = 64
+
+
+def sample_tokens(local_logits, vocab_off, temperature, top_p, top_k, uniform, ps):
+    """Per-rank top-64 candidates + (max, sum-exp) of the local vocab shard
+    (radix select), exchanged through the fused all-reduce slots when TP > 1
+    (NCCL all-gather of the small candidate buffer otherwise), then one
+    sorting / top-k / top-p / draw kernel per row."""
+    B, n = local_logits.shape
+    dev = local_logits.device
+    Kc = SAMPLE_CANDIDATES
+    temperature = temperature.float().contiguous()
+    top_p = top_p.float().contiguous()
+    top_k = top_k.to(torch.int32).contiguous()
+    uniform = uniform.float().contiguous()
+    tokens = torch.empty(B, dtype=torch.int64, device=dev)
+    world = ps.tp_size
+    far = getattr(ps, "fused_ar", None) if world > 1 else None
+    logits = local_logits if local_logits.stride(-1) == 1 else local_logits.contiguous()
+    if far is not None and far.world == world and B * (Kc + 1) * 8 <= far.max_tokens * far.hidden * 2:
+        _C.lm_candidates(logits, Kc, vocab_off, temperature, None, far.bases, far.rank, far.max_tokens, far.hidden,
+                         far.epoch, far.push_ticket)
+        _C.sample_final(None, B, Kc, world, far.bases, far.rank, far.max_tokens, far.hidden, far.epoch, far.ticket,
+                        temperature, top_p, top_k, uniform, tokens, far.err)
+        return tokens
+    cand = torch.empty(B, Kc + 1, dtype=torch.int64, device=dev)       # uint2 entries
+    _C.lm_candidates(logits, Kc, vocab_off, temperature, cand, [], 0, 0, 0, None, None)
+    if world > 1:
+        parts = [torch.empty_like(cand) for _ in range(world)]
+        dist.all_gather(parts, cand, group=ps.tp_group)
+        cand = torch.stack(parts)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    _C.sample_final(cand, B, Kc, world, [], 0, 0, 0, None, None, temperature, top_p, top_k, uniform, tokens, err)
+    return tokens
+
+
 def sample(logits, temperature, top_p, top_k, uniform):
     """Vectorised temperature / top-k / top-p sampling with given uniforms."""
     greedy = temperature <= 0

@@ -247,7 +247,8 @@ def main():
     e2e_value = args.batch * args.steps / (e2e_ms / 1e3)
     tpot_p50 = statistics.median(step_times) * 1e3
 
-    h2d = local_batch * (4 + 4 + 8 + 4) + local_batch * eng.graphs.max_pages * 4
+    # token id, position, KV slot, length, block-table row, sampling params (4 x 4 B)
+    h2d = local_batch * (4 + 4 + 8 + 4 + 16) + local_batch * eng.graphs.max_pages * 4
     d2h = local_batch * 8
     launches = count_launches(gr) if args.impl == "native" else None
     if os.environ.get("B200_BENCH_PROFILE") == "1":

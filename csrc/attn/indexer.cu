@@ -26,6 +26,7 @@
 // Reference parity: the reference calls DeepGEMM's prefill indexer and the
 // serving fork's top-k (ix.py:5-18, ct.py:8-14); these kernels are our own.
 #include "../common/ptx.cuh"
+#include "../common/radix_select.cuh"
 #include "attn.h"
 
 namespace b200 {
@@ -269,134 +270,22 @@ ix_score_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
 // ----------------------------------------------------------------------------
 // topk_select
 // ----------------------------------------------------------------------------
-constexpr int kTopkThreads = 1024;
-
-__device__ __forceinline__ uint32_t order_key(float f) {
-  const uint32_t u = __float_as_uint(f);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-
-// Exclusive block scan over 1024 threads; returns this thread's prefix and
-// writes the block total to *total.
-__device__ __forceinline__ int block_excl_scan(int v, int* warp_buf, int* total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int x = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= o) x += y;
-  }
-  if (lane == 31) warp_buf[warp] = x;
-  __syncthreads();
-  if (warp == 0) {
-    int w = warp_buf[lane];
-    int z = w;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, z, o);
-      if (lane >= o) z += y;
-    }
-    warp_buf[lane] = z - w;         // exclusive warp offsets
-    if (lane == 31) *total = z;
-  }
-  __syncthreads();
-  const int r = warp_buf[warp] + x - v;
-  __syncthreads();
-  return r;
-}
+constexpr int kTopkThreads = rsel::kThreads;
 
 __global__ void __launch_bounds__(kTopkThreads)
 topk_select_kernel(const float* scores, int64_t ld, const int* q_pos, int K, int* out) {
-  __shared__ int hist[256];
-  __shared__ int warp_buf[32];
-  __shared__ int s_total;
-  __shared__ int s_bin, s_rem;
+  __shared__ rsel::Smem sm;
   const int t = blockIdx.x;
-  const int tid = threadIdx.x;
   pdl_wait();
   pdl_launch_dependents();
   const int n = q_pos[t] + 1;
   int* o = out + (int64_t)t * K;
   if (n <= K) {
-    for (int i = tid; i < K; i += kTopkThreads) o[i] = i < n ? i : -1;
+    for (int i = threadIdx.x; i < K; i += kTopkThreads) o[i] = i < n ? i : -1;
     return;
   }
   const float* sc = scores + (int64_t)t * ld;
-  uint32_t prefix = 0, mask = 0;
-  int remaining = K;
-  for (int d = 3; d >= 0; --d) {
-    const int shift = 8 * d;
-    for (int i = tid; i < 256; i += kTopkThreads) hist[i] = 0;
-    __syncthreads();
-    // Scores of one query crowd into a few exponent bins, so lanes that hit
-    // the same bin combine their increments (one shared atomic per bin per
-    // warp instead of one per lane).
-    for (int i0 = 0; i0 < n; i0 += kTopkThreads) {
-      const int i = i0 + tid;
-      int bin = -1;
-      if (i < n) {
-        const uint32_t u = order_key(sc[i]);
-        if ((u & mask) == prefix) bin = (u >> shift) & 255;
-      }
-      const unsigned peers = __match_any_sync(0xffffffffu, bin);
-      if (bin >= 0 && (threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&hist[bin], __popc(peers));
-    }
-    __syncthreads();
-    if (tid < 32) {
-      // lane l owns bins 255-8l .. 248-8l (descending)
-      int c[8], sum = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        c[j] = hist[255 - 8 * tid - j];
-        sum += c[j];
-      }
-      int incl = sum;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, off);
-        if (tid >= off) incl += y;
-      }
-      const int above = incl - sum;      // count in bins above this lane's chunk
-      if (above < remaining && remaining <= incl) {
-        int acc = above;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (acc < remaining && remaining <= acc + c[j]) {
-            s_bin = 255 - 8 * tid - j;
-            s_rem = remaining - acc;
-          }
-          acc += c[j];
-        }
-      }
-    }
-    __syncthreads();
-    prefix |= uint32_t(s_bin) << shift;
-    mask |= 0xFFu << shift;
-    remaining = s_rem;
-    __syncthreads();
-  }
-  // prefix = key of the K-th largest score; take every larger score and the
-  // first `remaining` scores equal to it, in position order.
-  const int per = (n + kTopkThreads - 1) / kTopkThreads;
-  const int lo = min(n, tid * per), hi = min(n, lo + per);
-  int gt = 0, eq = 0;
-  for (int i = lo; i < hi; ++i) {
-    const uint32_t u = order_key(sc[i]);
-    gt += u > prefix;
-    eq += u == prefix;
-  }
-  const int eq_before = block_excl_scan(eq, warp_buf, &s_total);
-  const int take_eq = max(0, min(eq, remaining - eq_before));
-  int off = block_excl_scan(gt + take_eq, warp_buf, &s_total);
-  int taken = 0;
-  for (int i = lo; i < hi; ++i) {
-    const uint32_t u = order_key(sc[i]);
-    if (u > prefix || (u == prefix && taken < take_eq)) {
-      if (u == prefix) ++taken;
-      if (off < K) o[off] = i;
-      ++off;
-    }
-  }
+  rsel::select_topk([&](int i) { return __ldcg(sc + i); }, n, K, sm, [&](int slot, int i) { o[slot] = i; });
 }
 
 // ----------------------------------------------------------------------------

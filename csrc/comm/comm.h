@@ -12,6 +12,8 @@ struct ArPeers {
   int rank;
   int world;
   int max_t;                                // token rows per receive slot
+  int hidden = 0;                           // bf16 columns per slot row (kernels that reuse the
+                                            // slots as raw bytes need it to locate a slot)
 };
 
 inline int64_t ar_buffer_bytes(int world, int max_t, int hidden) {

@@ -4,6 +4,7 @@
 #include <torch/extension.h>
 
 #include "comm.h"
+#include "../elementwise/elementwise.h"
 
 namespace {
 
@@ -150,6 +151,50 @@ void ep_combine_rs(const at::Tensor& y, const at::Tensor& pair_row, int64_t T_st
   TORCH_CHECK(rc == 0, "ep_combine_rs failed ", rc);
 }
 
+// ---------------------------------------------------------------------------
+// Vocab-parallel sampling.  bases empty: local candidate buffers; else the
+// candidates travel through the fused all-reduce slots of those ranks.
+void lm_candidates(const at::Tensor& logits, int64_t Kc, int64_t vocab_off, const at::Tensor& temperature,
+                   c10::optional<at::Tensor> out, std::vector<int64_t> bases, int64_t rank, int64_t max_t,
+                   int64_t hidden, c10::optional<at::Tensor> epoch, c10::optional<at::Tensor> ticket) {
+  TORCH_CHECK(logits.is_cuda() && logits.dim() == 2 && logits.stride(1) == 1, "logits [B, n]");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat || logits.scalar_type() == at::kBFloat16, "logits fp32/bf16");
+  const c10::cuda::CUDAGuard g(logits.device());
+  ArPeers p{};
+  const bool fused = !bases.empty();
+  if (fused) {
+    p = make_peers(bases, rank, max_t);
+    p.hidden = hidden;
+  }
+  const int rc = b200_lm_candidates(logits.data_ptr(), logits.scalar_type() == at::kFloat, logits.stride(0),
+                                    logits.size(0), logits.size(1), Kc, vocab_off, temperature.data_ptr<float>(),
+                                    optr<void>(out), fused ? &p : nullptr,
+                                    fused ? reinterpret_cast<const uint32_t*>(epoch->data_ptr()) : nullptr,
+                                    fused ? reinterpret_cast<uint32_t*>(ticket->data_ptr()) : nullptr, cur());
+  TORCH_CHECK(rc == 0, "lm_candidates failed ", rc);
+}
+
+void sample_final(c10::optional<at::Tensor> cand, int64_t B, int64_t Kc, int64_t world, std::vector<int64_t> bases,
+                  int64_t rank, int64_t max_t, int64_t hidden, c10::optional<at::Tensor> epoch,
+                  c10::optional<at::Tensor> ticket, const at::Tensor& temperature, const at::Tensor& top_p,
+                  const at::Tensor& top_k, const at::Tensor& uniform, at::Tensor tokens, at::Tensor err) {
+  TORCH_CHECK(tokens.scalar_type() == at::kLong && top_k.scalar_type() == at::kInt, "tokens int64, top_k int32");
+  const c10::cuda::CUDAGuard g(tokens.device());
+  ArPeers p{};
+  const bool fused = !bases.empty();
+  if (fused) {
+    p = make_peers(bases, rank, max_t);
+    p.hidden = hidden;
+  }
+  const int rc = b200_sample_final(optr<void>(cand), B, Kc, world, fused ? &p : nullptr,
+                                   fused ? reinterpret_cast<uint32_t*>(epoch->data_ptr()) : nullptr,
+                                   fused ? reinterpret_cast<uint32_t*>(ticket->data_ptr()) : nullptr,
+                                   temperature.data_ptr<float>(), top_p.data_ptr<float>(), top_k.data_ptr<int>(),
+                                   uniform.data_ptr<float>(), tokens.data_ptr<int64_t>(),
+                                   reinterpret_cast<uint32_t*>(err.data_ptr()), cur());
+  TORCH_CHECK(rc == 0, "sample_final failed ", rc);
+}
+
 }  // namespace
 
 void register_comm(pybind11::module& m) {
@@ -162,4 +207,6 @@ void register_comm(pybind11::module& m) {
   m.def("ep_align", &ep_align);
   m.def("ep_gather", &ep_gather);
   m.def("ep_combine_rs", &ep_combine_rs);
+  m.def("lm_candidates", &lm_candidates);
+  m.def("sample_final", &sample_final);
 }

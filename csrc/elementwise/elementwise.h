@@ -27,3 +27,14 @@ int b200_nvfp4_quant(const void* x, int f32, int64_t ld, int T, int K, uint8_t* 
                      cudaStream_t st);
 int b200_moe_gather4(const uint8_t* xq, const uint8_t* xsf, const float* xg, const int* pair_row, int npairs, int K,
                      int Kx, uint8_t* dq, uint8_t* dsf, float* dg, cudaStream_t st);
+
+// Vocab-parallel sampling (see sample.cu).  peers == nullptr: local buffers
+// (out / cand = [world][B][Kc + 1] uint2); else candidates travel through
+// the fused all-reduce's receive slots (ArPeers from comm/comm.h).
+struct ArPeers;
+int b200_lm_candidates(const void* logits, int f32, int64_t ld, int B, int n, int Kc, int vocab_off,
+                       const float* temperature, void* out, const ArPeers* peers, const uint32_t* epoch,
+                       uint32_t* ticket, cudaStream_t st);
+int b200_sample_final(const void* cand, int B, int Kc, int world, const ArPeers* peers, uint32_t* epoch,
+                      uint32_t* ticket, const float* temperature, const float* top_p, const int* top_k,
+                      const float* uniform, int64_t* tokens, uint32_t* err, cudaStream_t st);

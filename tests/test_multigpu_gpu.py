@@ -45,6 +45,11 @@ def _rank(rank, world, comm_impl, kind):
     m.allocate_kv(8)
     fb = _batch(cfg, ps.device)
     out = m.forward(fb).float().cpu()
+    # device sampling without gathering the logits (candidates exchanged over
+    # the fused slots or NCCL): greedy rows must pick this run's argmax
+    z = torch.zeros(2, device=ps.device)
+    toks = m.forward_tokens(_batch(cfg, ps.device), z, z + 1, z.int(), z).cpu()
+    assert toks.tolist() == out.argmax(-1).tolist(), (toks, out.argmax(-1))
     ref = None
     if rank == 0:
         single = ParallelState(device=ps.device)
