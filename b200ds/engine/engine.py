@@ -196,6 +196,9 @@ class Engine:
         for obj in (getattr(self.ps, "fused_ar", None), getattr(self.ps, "fused_ep", None)):
             if obj is not None:
                 obj.check()
+        if self.device.type == "cuda" and ops.get_impl() == "native":
+            from ..ops import cuda as _cuda
+            _cuda.check_device_errors()
 
     def generate(self, prompts: Sequence[Union[str, Sequence[int]]],
                  params: Union[SamplingParams, Sequence[SamplingParams], None] = None) -> List[GenerateOutput]:

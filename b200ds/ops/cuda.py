@@ -6,6 +6,7 @@ extension raises: there is no silent fallback.
 from __future__ import annotations
 
 import math
+import os
 from typing import Optional
 
 import torch
@@ -247,6 +248,58 @@ def moe_tile_n(rows_per_expert: float, cap: int) -> int:
     return cap
 
 
+MOE_FUSED = os.environ.get("B200_MOE_FUSED", "1") != "0"
+
+
+def _moe_ws(ex, dev) -> torch.Tensor:
+    """Work counters of the fused expert kernel ([2 + E] int32, zero; the
+    kernel leaves them zero)."""
+    ws = getattr(ex, "_fused_ws", None)
+    if ws is None or ws.device != dev:
+        ws = torch.zeros(2 + ex.count, dtype=torch.int32, device=dev)
+        ex._fused_ws = ws
+        ex._fused_err = torch.zeros(1, dtype=torch.int32, device=dev)
+        _ERR_WORDS.append(ex._fused_err)
+    return ws
+
+
+_ERR_WORDS = []     # device error words of kernels with in-kernel waits
+
+
+def check_device_errors() -> None:
+    """Raise if a bounded in-kernel wait (dependency between CTAs) ran out."""
+    for e in _ERR_WORDS:
+        v = int(e.item())
+        if v:
+            raise RuntimeError(f"fused expert GEMM: in-kernel dependency wait timed out (code {v})")
+
+
+def _expert_gemms(ex, xq, xsf, xg, hq, hsf, y, Hd, bn1, bn2, seg_start, seg_count, tt1, tt2, row_weight, fp4):
+    """FC1 (SwiGLU + requant into hq) and FC2 (routing-weighted into y): one
+    fused persistent launch when both use the same token tile (decode), else
+    two grouped launches."""
+    E, I = ex.count, ex.inter
+    w13, w2 = ex.w13, ex.w2
+    g2 = float(ex.fc2_act_scale)
+    if MOE_FUSED and bn1 == bn2:
+        ws = _moe_ws(ex, y.device)
+        _C.moe_fused(w13.data, w13.sf, w2.data, w2.sf, xq, xsf, hq, hsf, y, E, Hd, I, bn1, seg_start, seg_count, tt1,
+                     row_weight, ws, ex._fused_err, 0, True, ex.tiled,
+                     xg if fp4 else None, w13.global_scale if fp4 else None, w2.global_scale if fp4 else None, g2)
+        return
+    if fp4:
+        _C.gemm_grouped(w13.data, w13.sf, xq, xsf, 2 * I, Hd, E, I, bn1, seg_start, seg_count, tt1, 2,
+                        None, 0, hq, hsf, I, None, 0, True, w_g=w13.global_scale, x_g=xg, out_g=g2, a_tiled=ex.tiled)
+        _C.gemm_grouped(w2.data, w2.sf, hq, hsf, Hd, I, E, 0, bn2, seg_start, seg_count, tt2, 3,
+                        y, Hd, None, None, 0, row_weight, 0, True, w_g=w2.global_scale, x_g_const=g2, a_tiled=ex.tiled)
+        return
+    _C.gemm_grouped(w13.data, w13.sf, xq, xsf, 2 * I, Hd, E, I, bn1, seg_start, seg_count, tt1, 2,
+                    None, 0, hq, hsf, I, None, 0, True, a_tiled=ex.tiled)
+    _C.gemm_grouped(w2.data, w2.sf, hq, hsf, Hd, I, E, 0, bn2, seg_start, seg_count, tt2, 3,
+                    y, Hd, None, None, 0, row_weight, 0, True, a_tiled=ex.tiled)
+
+
+
 def moe_experts(h, w: torch.Tensor, ids: torch.Tensor, ex, out_dtype=torch.bfloat16, n_experts_total=None,
                 combine: bool = True):
     """Local-expert MoE: routing layout -> row gather -> persistent FC1
@@ -278,12 +331,9 @@ def moe_experts(h, w: torch.Tensor, ids: torch.Tensor, ex, out_dtype=torch.bfloa
     xs = alloc_qact(max_rows, Hd, dev)
     _C.moe_gather(a.q, a.sf, pair_row, xs.q, xs.sf)
     hq = alloc_qact(max_rows, I, dev)
-    w13, w2 = ex.w13, ex.w2
-    _C.gemm_grouped(w13.data, w13.sf, xs.q, xs.sf, 2 * I, Hd, E, I, bn1, seg_start, seg_count, tt1, 2,
-                    None, 0, hq.q, hq.sf, I, None, 0, True, a_tiled=ex.tiled)
     y = torch.empty(max_rows, Hd, dtype=torch.bfloat16, device=dev)
-    _C.gemm_grouped(w2.data, w2.sf, hq.q, hq.sf, Hd, I, E, 0, bn2, seg_start, seg_count, tt2, 3,
-                    y, Hd, None, None, 0, row_weight, 0, True, a_tiled=ex.tiled)
+    _expert_gemms(ex, xs.q, xs.sf, None, hq.q, hq.sf, y, Hd, bn1, bn2, seg_start, seg_count, tt1, tt2, row_weight,
+                  False)
     if not combine:
         from . import MoEPartial
         return MoEPartial(y, pair_row, None)
@@ -341,13 +391,8 @@ def moe_experts_nvfp4(h, w, ids, ex, out_dtype=torch.bfloat16, n_experts_total=N
     _C.moe_gather4(xq, xsf, xg, pair_row, xs_q, xs_sf, xs_g)
     hq = torch.empty(max_rows, I // 2, dtype=torch.uint8, device=dev)
     hsf = torch.empty(max_rows * (I // 16), dtype=torch.uint8, device=dev)
-    w13, w2 = ex.w13, ex.w2
-    g2 = float(ex.fc2_act_scale)
-    _C.gemm_grouped(w13.data, w13.sf, xs_q, xs_sf, 2 * I, Hd, E, I, bn1, seg_start, seg_count, tt1, 2,
-                    None, 0, hq, hsf, I, None, 0, True, w_g=w13.global_scale, x_g=xs_g, out_g=g2, a_tiled=ex.tiled)
     y = torch.empty(max_rows, Hd, dtype=torch.bfloat16, device=dev)
-    _C.gemm_grouped(w2.data, w2.sf, hq, hsf, Hd, I, E, 0, bn2, seg_start, seg_count, tt2, 3,
-                    y, Hd, None, None, 0, row_weight, 0, True, w_g=w2.global_scale, x_g_const=g2, a_tiled=ex.tiled)
+    _expert_gemms(ex, xs_q, xs_sf, xs_g, hq, hsf, y, Hd, bn1, bn2, seg_start, seg_count, tt1, tt2, row_weight, True)
     if not combine:
         from . import MoEPartial
         return MoEPartial(y, pair_row, None)
@@ -404,20 +449,15 @@ def moe_experts_ep(h, w, ids, ex, T_step: int, n_experts_total: int, ep):
                      ep.gather_ticket)
         hq = torch.empty(max_rows, I // 2, dtype=torch.uint8, device=dev)
         hsf = torch.empty(max_rows * (I // 16), dtype=torch.uint8, device=dev)
-        g2 = float(ex.fc2_act_scale)
-        _C.gemm_grouped(w13.data, w13.sf, xs_q, xs_sf, 2 * I, Hd, E, I, bn1, seg_start, seg_count, tt1, 2,
-                        None, 0, hq, hsf, I, None, 0, True, w_g=w13.global_scale, x_g=xs_g, out_g=g2, a_tiled=ex.tiled)
-        _C.gemm_grouped(w2.data, w2.sf, hq, hsf, Hd, I, E, 0, bn2, seg_start, seg_count, tt2, 3,
-                        y, Hd, None, None, 0, row_weight, 0, True, w_g=w2.global_scale, x_g_const=g2, a_tiled=ex.tiled)
+        _expert_gemms(ex, xs_q, xs_sf, xs_g, hq, hsf, y, Hd, bn1, bn2, seg_start, seg_count, tt1, tt2, row_weight,
+                      True)
         return EPPartial(y, pair_row, T_step, T_r)
     xs = alloc_qact(max_rows, Hd, dev)
     _C.ep_gather(ep.bases, ep.rank, ep.max_t, Hd, K, T_step, pair_row, xs.q, xs.sf, None, ep.epoch,
                  ep.gather_ticket)
     hq = alloc_qact(max_rows, I, dev)
-    _C.gemm_grouped(w13.data, w13.sf, xs.q, xs.sf, 2 * I, Hd, E, I, bn1, seg_start, seg_count, tt1, 2,
-                    None, 0, hq.q, hq.sf, I, None, 0, True, a_tiled=ex.tiled)
-    _C.gemm_grouped(w2.data, w2.sf, hq.q, hq.sf, Hd, I, E, 0, bn2, seg_start, seg_count, tt2, 3,
-                    y, Hd, None, None, 0, row_weight, 0, True, a_tiled=ex.tiled)
+    _expert_gemms(ex, xs.q, xs.sf, None, hq.q, hq.sf, y, Hd, bn1, bn2, seg_start, seg_count, tt1, tt2, row_weight,
+                  False)
     return EPPartial(y, pair_row, T_step, T_r)
 
 

@@ -104,7 +104,7 @@ def _moe_layout(T, K, E_total, E_local, dev, bn1, bn2):
                 row_weight=row_weight, pair_row=pair_row, active=active)
 
 
-def run_moe(fmt: str, T: int, E_total: int, E_local: int, iters: int, h=7168, I=2048, tiled=False):
+def run_moe(fmt: str, T: int, E_total: int, E_local: int, iters: int, h=7168, I=2048, tiled=False, fused=False):
     from b200ds import _C
     from b200ds.ops import cuda
     from b200ds.models.random_init import _Seeder, rand_mx, rand_nvfp4
@@ -148,6 +148,20 @@ def run_moe(fmt: str, T: int, E_total: int, E_local: int, iters: int, h=7168, I=
                                       a_tiled=tiled)
         peak = 2 * BF16
     pairs = int((L["pair_row"] >= 0).sum())
+    if fused:
+        from b200ds.ops import ExpertWeights
+        ex = ExpertWeights(0, E_local, w13, w2, I, tiled=tiled, fc2_act_scale=1 / 32)
+        if fp4:
+            fn = lambda: cuda._expert_gemms(ex, xs_q, xs_sf, xs_g, hq, hsf, y, h, bn1, bn1, L["seg_start"],
+                                            L["seg_count"], L["tt1"], L["tt2"], L["row_weight"], True)
+        else:
+            fn = lambda: cuda._expert_gemms(ex, xs.q, xs.sf, None, hqa.q, hqa.sf, y, h, bn1, bn1, L["seg_start"],
+                                            L["seg_count"], L["tt1"], L["tt2"], L["row_weight"], False)
+        t = timed(fn, iters)
+        shape = f"{fmt} T={T} top8 E={E_local}/{E_total} active={L['active']} pairs={pairs}" + (" tiled" if tiled else "")
+        report(f"moe_fc1fc2_fused_{fmt}", shape, t, nbytes=L["active"] * wbytes, flops=2 * pairs * 3 * I * h,
+               flop_peak=peak, note=f"bn={bn1}, one launch")
+        return
     shape = f"{fmt} T={T} top8 E={E_local}/{E_total} active={L['active']} pairs={pairs}" + (" tiled" if tiled else "")
     t1 = timed(fc1, iters)
     report(f"moe_fc1_{fmt}", shape, t1, nbytes=L["active"] * wbytes * 2 / 3, flops=2 * pairs * 2 * I * h,
@@ -256,6 +270,11 @@ def main():
         ("moe_mxfp8_T64_ep8", lambda: run_moe("mxfp8", 64, 256, 32, a.iters)),
         ("moe_nvfp4_T256_ep8", lambda: run_moe("nvfp4", 256, 256, 32, a.iters)),
         ("moe_nvfp4_T64_ep1", lambda: run_moe("nvfp4", 64, 256, 64 if small else 256, a.iters)),
+        # FC1 + FC2 in one persistent launch (dynamic work grabbing, FC2 fills FC1's tail)
+        ("moe_mxfp8_T64_ep1_fused", lambda: run_moe("mxfp8", 64, 256, 64 if small else 256, a.iters, fused=True)),
+        ("moe_mxfp8_T64_ep8_fused", lambda: run_moe("mxfp8", 64, 256, 32, a.iters, tiled=True, fused=True)),
+        ("moe_nvfp4_T256_ep8_fused", lambda: run_moe("nvfp4", 256, 256, 32, a.iters, tiled=True, fused=True)),
+        ("moe_nvfp4_T64_ep1_fused", lambda: run_moe("nvfp4", 64, 256, 64 if small else 256, a.iters, fused=True)),
         # the same with weights stored as contiguous 128 x 128-byte tiles
         ("moe_mxfp8_T64_ep1_tiled", lambda: run_moe("mxfp8", 64, 256, 64 if small else 256, a.iters, tiled=True)),
         ("moe_mxfp8_T64_ep8_tiled", lambda: run_moe("mxfp8", 64, 256, 32, a.iters, tiled=True)),

@@ -4,6 +4,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
+#include <algorithm>
 
 #include <cstring>
 #include <vector>
@@ -241,6 +242,52 @@ void gemm_grouped(const at::Tensor& w, const at::Tensor& w_sf, const at::Tensor&
   check(b200_gemm_grouped(&a, cur_stream()), "gemm_grouped");
 }
 
+void moe_fused(const at::Tensor& w13, const at::Tensor& w13_sf, const at::Tensor& w2, const at::Tensor& w2_sf,
+               const at::Tensor& x, const at::Tensor& x_sf, at::Tensor hq, at::Tensor hq_sf, at::Tensor y, int64_t E,
+               int64_t hidden, int64_t inter, int64_t bn, const at::Tensor& seg_start, const at::Tensor& seg_count,
+               const at::Tensor& ttile_off, const at::Tensor& row_weight, at::Tensor ws, at::Tensor err,
+               int64_t num_ctas, bool pdl, bool a_tiled, c10::optional<at::Tensor> x_g, c10::optional<at::Tensor> w1_g,
+               c10::optional<at::Tensor> w2_g, double out_g) {
+  check_cuda(w13, "w13");
+  const c10::cuda::CUDAGuard gd(w13.device());
+  TORCH_CHECK(ws.scalar_type() == at::kInt && ws.numel() >= 2 + E, "workspace int32 [2 + E]");
+  TORCH_CHECK(y.scalar_type() == at::kBFloat16 && y.is_contiguous(), "y bf16");
+  MoeFusedArgs a{};
+  a.w13 = ptr<uint8_t>(w13);
+  a.w13_sf = ptr<uint8_t>(w13_sf);
+  a.w13_sf_estride = w13_sf.dim() > 1 ? w13_sf.stride(0) : 0;
+  a.w2 = ptr<uint8_t>(w2);
+  a.w2_sf = ptr<uint8_t>(w2_sf);
+  a.w2_sf_estride = w2_sf.dim() > 1 ? w2_sf.stride(0) : 0;
+  a.x = ptr<uint8_t>(x);
+  a.x_sf = ptr<uint8_t>(x_sf);
+  a.hq = ptr<uint8_t>(hq);
+  a.hq_sf = ptr<uint8_t>(hq_sf);
+  a.y = y.data_ptr();
+  a.ldy = y.stride(0);
+  a.rows = std::min<int64_t>(x.size(0), hq.size(0));
+  a.hidden = hidden;
+  a.inter = inter;
+  a.E = E;
+  a.bn = bn;
+  a.seg_start = ptr<int>(seg_start);
+  a.seg_count = ptr<int>(seg_count);
+  a.ttile_off = ptr<int>(ttile_off);
+  a.row_weight = ptr<float>(row_weight);
+  a.work = ptr<int>(ws);
+  a.fc1_done = ptr<int>(ws) + 2;
+  a.err = reinterpret_cast<uint32_t*>(err.data_ptr());
+  a.num_ctas = num_ctas > 0 ? num_ctas : num_sms();
+  a.pdl = pdl ? 1 : 0;
+  a.a_tiled = a_tiled ? 1 : 0;
+  a.fp4 = (w1_g.has_value() && w1_g->defined()) ? 1 : 0;
+  a.x_g = optr<float>(x_g);
+  a.w1_g = optr<float>(w1_g);
+  a.w2_g = optr<float>(w2_g);
+  a.out_g = float(out_g);
+  check(b200_moe_fused(&a, cur_stream()), "moe_fused");
+}
+
 void nvfp4_quant(const at::Tensor& x, at::Tensor q, at::Tensor sf, at::Tensor g) {
   check_cuda(x, "x");
   const c10::cuda::CUDAGuard gd(x.device());
@@ -324,6 +371,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("w_g") = pybind11::none(), pybind11::arg("x_g") = pybind11::none(),
         pybind11::arg("x_g_const") = 1.0, pybind11::arg("out_g") = 1.0, pybind11::arg("a_tiled") = false);
   m.def("nvfp4_quant", &nvfp4_quant);
+  m.def("moe_fused", &moe_fused);
   m.def("moe_gather4", &moe_gather4);
   m.def("num_sms", &num_sms);
   m.def("graph_kernel_count", &graph_kernel_count);

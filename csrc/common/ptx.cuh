@@ -53,6 +53,7 @@ enum : uint32_t {
   kErrMbarTimeout = 1,
   kErrPeerTimeout = 2,
   kErrBadArg = 3,
+  kErrDepTimeout = 4,     // an in-kernel dependency (another CTA's work) did not arrive in time
 };
 
 // Wall-clock budget for any single wait inside a kernel (ns).

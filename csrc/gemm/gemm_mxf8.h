@@ -89,3 +89,37 @@ struct GroupedArgs {
   float out_g;
 };
 int b200_gemm_grouped(const GroupedArgs* args, cudaStream_t stream);
+
+// Fused persistent FC1 + FC2 of the routed experts (see moe_fused.cu).
+struct MoeFusedArgs {
+  const uint8_t* w13;      // [E, 2 * inter, hidden] (MXFP8 e4m3 or NVFP4 pairs; optionally tiled)
+  const uint8_t* w13_sf;
+  int64_t w13_sf_estride;
+  const uint8_t* w2;       // [E, hidden, inter]
+  const uint8_t* w2_sf;
+  int64_t w2_sf_estride;
+  const uint8_t* x;        // sorted activation rows [rows, hidden]
+  const uint8_t* x_sf;
+  uint8_t* hq;             // FC1 output / FC2 operand [rows, inter]
+  uint8_t* hq_sf;
+  void* y;                 // bf16 [rows, ldy]
+  int ldy;
+  int64_t rows;
+  int hidden, inter, E, bn;
+  const int* seg_start;
+  const int* seg_count;
+  const int* ttile_off;    // [E+1] prefix of ceil(count / bn)
+  const float* row_weight;
+  int* work;               // [2] zero before the first launch; the kernel resets it
+  int* fc1_done;           // [E] idem
+  uint32_t* err;
+  int num_ctas;
+  int pdl;
+  int a_tiled;
+  int fp4;
+  const float* x_g;        // NVFP4: per sorted row
+  const float* w1_g;       // NVFP4: per expert
+  const float* w2_g;
+  float out_g;             // NVFP4: global scale of the FC1 output
+};
+int b200_moe_fused(const MoeFusedArgs* args, cudaStream_t stream);

@@ -549,3 +549,45 @@ def test_sample_tokens_matches_reference(V):
                                u.to(DEV), ParallelState(device=torch.device(DEV)))
     exp16 = ref.sample(logits.to(torch.bfloat16).float(), temp, top_p, top_k, u)
     assert got16.cpu().tolist() == exp16.tolist()
+
+
+@pytest.mark.parametrize("fp4,tiled", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("T,skew", [(5, False), (64, False), (37, True), (200, False)])
+def test_moe_fused_matches_two_launch(fp4, tiled, T, skew):
+    """The fused persistent FC1+FC2 kernel (dynamic work grabbing, per-expert
+    FC1 -> FC2 dependencies) gives bit-identical outputs to the two grouped
+    launches, also when every token goes to a few experts."""
+    from b200ds.ops import ExpertWeights, cuda
+    from b200ds.ops.quant import MXFP8Tensor, NVFP4Tensor, tile_rows128
+    torch.manual_seed(7)
+    H, I, E, K = 1024, 256, 16, 4
+    if fp4:
+        w13, w2 = _nvfp4_stack(E, 2 * I, H), _nvfp4_stack(E, H, I)
+        tile = lambda t: NVFP4Tensor(tile_rows128(t.data), t.sf, t.global_scale, t.rows)
+    else:
+        mk = lambda N, Kd: [_mx(torch.randn(N, Kd, device=DEV) * 0.05) for _ in range(E)]
+        a13, a2 = mk(2 * I, H), mk(H, I)
+        w13 = MXFP8Tensor(torch.stack([w.data for w in a13]), torch.stack([w.sf for w in a13]))
+        w2 = MXFP8Tensor(torch.stack([w.data for w in a2]), torch.stack([w.sf for w in a2]))
+        tile = lambda t: MXFP8Tensor(tile_rows128(t.data.view(torch.uint8)).view(t.data.dtype), t.sf, t.rows)
+    ex = ExpertWeights(0, E, tile(w13) if tiled else w13, tile(w2) if tiled else w2, I, tiled=tiled)
+    x = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    if skew:
+        ids = (torch.arange(K, device=DEV, dtype=torch.int32) * 3).repeat(T, 1)
+    else:
+        ids = torch.stack([torch.randperm(E, device=DEV)[:K] for _ in range(T)]).int()
+    wts = torch.rand(T, K, device=DEV)
+    run = (lambda: cuda.moe_experts_nvfp4(x, wts, ids, ex, torch.float32)) if fp4 else \
+        (lambda: cuda.moe_experts(cuda.quant(x), wts, ids, ex, torch.float32))
+    old = cuda.MOE_FUSED
+    try:
+        cuda.MOE_FUSED = False
+        a = run()
+        cuda.MOE_FUSED = True
+        b = run()
+        c = run()                  # counters reset by the previous launch
+    finally:
+        cuda.MOE_FUSED = old
+    torch.cuda.synchronize()
+    cuda.check_device_errors()
+    assert torch.equal(a, b) and torch.equal(b, c)
