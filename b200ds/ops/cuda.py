@@ -182,12 +182,27 @@ def kv_store(kv_a, ln_w, eps, table, pos, cache, slots, kv_scale, kv_lora):
     _C.kv_store(kv_a, ln_w, eps, pos, table, slots, cache.view(torch.uint8), kv_scale, kv_lora)
 
 
+MLA_SPLITS = int(os.environ.get("B200_MLA_SPLITS", "0"))     # diagnostics: fixed KV splits
+MLA_HB = int(os.environ.get("B200_MLA_HB", "0"))             # diagnostics: fixed heads per CTA
+
+
+def mla_hb(H: int) -> int:
+    if MLA_HB and H % MLA_HB == 0:
+        return MLA_HB
+    return 64 if H % 64 == 0 else (32 if H % 32 == 0 else 16)
+
+
 def mla_splits(T: int, H: int, max_len: int) -> int:
     """KV splits so that decode grids cover the SMs (at least ~2 tiles each)."""
-    groups = H // 64 if H % 64 == 0 else (H // 32 if H % 32 == 0 else H // 16)
+    if MLA_SPLITS:
+        return MLA_SPLITS
+    # Split only up to one wave of CTAs: the split partials and their merge
+    # cost more than a longer per-CTA tile loop (measured: 64 x 1K, 128 heads
+    # 91 us unsplit vs 163 us in 3 splits; 16 heads best at 2 splits).
+    groups = H // mla_hb(H)
     ctas = T * max(1, groups)
-    s = max(1, min(16, -(-296 // ctas), max(1, max_len // 256)))
-    return s
+    tiles = max(1, -(-max_len // 128))
+    return max(1, min(16, 148 // max(ctas, 1), tiles // 2))
 
 
 def mla_attention(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size, topk=None, impl=None):
@@ -215,7 +230,7 @@ def mla_attention(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size, to
         po = torch.empty(nsplit, T, H, L, dtype=torch.float32, device=dev)
         pl = torch.empty(nsplit, T, H, dtype=torch.float32, device=dev)
     _C.mla_tc(q8, qs, cache.view(torch.uint8), kv_scale, fb.block_table, fb.q_seq, fb.positions, page_size,
-              softmax_scale, nsplit, out, po, pl, topk)
+              softmax_scale, nsplit, out, po, pl, topk, mla_hb(H))
     return out
 
 

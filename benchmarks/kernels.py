@@ -199,7 +199,19 @@ def run_mla(B: int, ctx: int, H: int, iters: int, topk: int = 0):
     flops = 2 * B * H * keys * (576 + 512)
     report("mla_sparse" if topk else "mla_decode", f"B={B} ctx={ctx} H={H}" + (f" top{topk}" if topk else ""), t,
            nbytes=nbytes, flops=flops, flop_peak=2 * BF16,
-           note=f"splits={cuda.mla_splits(B, H, keys)} incl. q quant + merge")
+           note=f"splits={cuda.mla_splits(B, H, keys)} hb={cuda.mla_hb(H)} incl. q quant + merge")
+
+
+def mla_sweep(B: int, ctx: int, H: int, iters: int):
+    """MLA decode time over KV splits x heads per CTA (diagnostic)."""
+    from b200ds.ops import cuda
+    for hb in (16, 32, 64):
+        if H % hb:
+            continue
+        for ns in (1, 2, 3, 4, 6, 8):
+            cuda.MLA_HB, cuda.MLA_SPLITS = hb, ns
+            run_mla(B, ctx, H, iters)
+    cuda.MLA_HB, cuda.MLA_SPLITS = 0, 0
 
 
 def run_indexer(B: int, ctx: int, iters: int):
@@ -282,6 +294,8 @@ def main():
         ("moe_nvfp4_T64_ep1_tiled", lambda: run_moe("nvfp4", 64, 256, 64 if small else 256, a.iters, tiled=True)),
         ("mla_decode_B64_1k_H128", lambda: run_mla(64, 1040, 128, a.iters)),
         ("mla_decode_B64_1k_H16", lambda: run_mla(64, 1040, 16, a.iters)),
+        ("mla_sweep_B64_1k_H128", lambda: mla_sweep(64, 1040, 128, a.iters)),
+        ("mla_sweep_B64_1k_H16", lambda: mla_sweep(64, 1040, 16, a.iters)),
         ("mla_sparse_B8_32k_H128", lambda: run_mla(8, 8192 if small else 32768, 128, a.iters, topk=2048)),
         ("indexer_B8_32k", lambda: run_indexer(8, 8192 if small else 32768, a.iters)),
         ("gemm_qkv_a_T64", lambda: run_gemm("qkv_a", 64, 2176, 7168, a.iters)),

@@ -27,6 +27,7 @@ struct MlaTcArgs {
   uint32_t* err;
   const int* topk = nullptr;  // [T, topk_n] cache positions (-1 = none): sparse MLA
   int topk_n = 0;
+  int hb = 0;                 // heads per CTA (16 / 32 / 64); 0 = largest that divides H
 };
 // Lightning indexer (sparse MLA): key store, query quantisation, tcgen05
 // scores and the top-k radix select.

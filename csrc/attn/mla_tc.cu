@@ -16,8 +16,10 @@
 // TMEM for the whole split; the epilogue normalises by the running sum and
 // writes bf16 (or a partial + log-sum-exp for the split merge).
 //
-// Warp roles (192 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA
-// issuer, warps 2-5 softmax / correction / epilogue.  All waits bounded.
+// Warp roles (320 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA
+// issuer, warps 2-9 softmax / correction / epilogue (two warps per TMEM
+// subpartition, each owning half of the head columns: the per-tile softmax
+// is the kernel's critical path).  All waits bounded.
 //
 // Sparse variant (SPARSE = true): the query attends only to the cache
 // positions in its top-k list (-1 = unused entry).  The KV rows of a tile are
@@ -37,7 +39,8 @@
 namespace b200 {
 namespace mla {
 
-constexpr int kThreads = 192;
+constexpr int kSmThreads = 256;      // softmax / epilogue threads (warps 2-9)
+constexpr int kThreads = 64 + kSmThreads;
 constexpr int kTile = 128;          // KV tokens per tile
 constexpr int kPage = 64;           // tokens per KV page (one TMA box height)
 constexpr int kL = 512;             // latent
@@ -59,11 +62,17 @@ struct Smem {
   static constexpr int kOffQ = 0;
   static constexpr int kOffKV = ((kQLat + kQRope + 1023) / 1024) * 1024;
   static constexpr int kOffP = kOffKV + kStages * kKVStage;
-  static constexpr int kOffS = kOffP + ((kP + 127) / 128) * 128;
-  static constexpr int kOffRed = kOffS + kS;            // 2 x 128 floats
-  static constexpr int kOffHead = kOffRed + 2 * 128 * 4;  // per-head state
+  static constexpr int kPPad = ((kP + 127) / 128) * 128;
+  // P^T double-buffered (softmax of tile i overlaps MMA2 of tile i - 1) when
+  // it fits next to two KV stages; 64-head groups keep one buffer.
+  static constexpr int kPB = (kOffP + 2 * kPPad + kTile * (HB + 1) * 4 + 2 * kSmThreads * 4 + 8 * HB * 4 + 256 + 1024
+                              <= 227 * 1024) ? 2 : 1;
+  static constexpr int kOffS = kOffP + kPB * kPPad;
+  static constexpr int kOffRed = kOffS + kS;            // 2 x kSmThreads floats
+  static constexpr int kOffHead = kOffRed + 2 * kSmThreads * 4;  // per-head state
   static constexpr int kOffBar = kOffHead + 8 * HB * 4;
   static constexpr int kBytes = kOffBar + 256 + 1024;
+  static_assert(kBytes <= 227 * 1024, "shared memory");
   static constexpr int kTmemS = 0;                      // 2 x HB columns
   static constexpr int kTmemO = 2 * HB;                 // 4 x HB columns
   static constexpr int kTmemNeed = 6 * HB;
@@ -114,9 +123,9 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
   uint64_t* q_full = bars + 4;
   uint64_t* s_full = bars + 5;           // [2]
   uint64_t* s_free = bars + 7;           // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* o_done = bars + 10;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* p_full = bars + 9;           // [2] P^T buffer (i & 1) written
+  uint64_t* o_done = bars + 11;          // [2] MMA2 of tile i (i & 1) complete
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 13);
 
   const int warp = warp_id(), lane = lane_id();
   const int t = blockIdx.x;
@@ -144,8 +153,10 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
       mbar_init(&s_free[i], 1);
     }
     mbar_init(q_full, 1);
-    mbar_init(p_full, 1);
-    mbar_init(o_done, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&p_full[i], 1);
+      mbar_init(&o_done[i], 1);
+    }
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -222,12 +233,12 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
     const uint32_t idesc2 = idesc_f8(128, HB, true, true);
     bool ok = nt > 0 && mbar_wait(q_full, 0, p.err);
     auto mma2 = [&](int i) -> bool {
-      if (!mbar_wait(p_full, i & 1, p.err)) return false;
+      if (!mbar_wait(&p_full[i & 1], (i >> 1) & 1, p.err)) return false;
       tc_fence_after();
       if (lane == 0) {
         const int s = i % kStages;
         const uint32_t kv = smem_u32(sKV + s * S::kKVStage);
-        const uint32_t pb = smem_u32(sP);
+        const uint32_t pb = smem_u32(sP + (i % S::kPB) * S::kPPad);
         for (int c = 0; c < 4; ++c) {
           for (int kk = 0; kk < kTile / 32; ++kk) {
             // A = V^T: MN-major SW128, 8-token groups 1024 B apart
@@ -237,7 +248,7 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
             mma_f8(tmem + S::kTmemO + c * HB, ad, bd, idesc2, (i > 0 || kk > 0) ? 1u : 0u);
           }
         }
-        mma_commit(o_done);
+        mma_commit(&o_done[i & 1]);
         mma_commit(&kv_empty[s]);
       }
       __syncwarp();
@@ -268,10 +279,11 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
     if (ok && nt > 0) mma2(nt - 1);
   } else {
     // ---------------------- softmax / correction / epilogue ----------------------
-    const int tid = threadIdx.x - 64;            // 0..127
+    const int tid = threadIdx.x - 64;            // 0..255
     const int sub = warp & 3;                    // TMEM subpartition
+    const int hc0 = ((warp - 2) >> 2) * (HB / 2);   // this warp's half of the head columns
     const int row = sub * 32 + lane;             // token row of S^T / latent row of O^T
-    constexpr int QN = 128 / HB;                 // threads per head in the reduction
+    constexpr int QN = kSmThreads / HB;          // threads per head in the reduction
     const int hh = tid % HB, part = tid / HB;
     if (tid < HB) {
       sHead[tid] = p.q_scale[(int64_t)t * p.H + h0 + tid] * p.qk_factor;
@@ -279,7 +291,7 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
       sHead[2 * HB + tid] = 0.f;
     }
     if (tid == 0) sFlag[0] = 0;
-    named_bar(1, 128);
+    named_bar(1, kSmThreads);
     bool ok = true;
     for (int i = 0; i < nt; ++i) {
       if (!mbar_wait(&s_full[i & 1], (i >> 1) & 1, p.err)) { ok = false; break; }
@@ -289,9 +301,9 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
       {
         const uint32_t base = tmem + S::kTmemS + (i & 1) * HB + (uint32_t(sub * 32) << 16);
 #pragma unroll
-        for (int c0 = 0; c0 < HB; c0 += 16) {
-          uint32_t r[16];
-          tmem_ld_x16(base + c0, r);
+        for (int c0 = hc0; c0 < hc0 + HB / 2; c0 += 8) {
+          uint32_t r[8];
+          tmem_ld_x8(base + c0, r);
           tmem_ld_wait();
           bool valid = tok0 + row < k_hi;
           if (SPARSE && valid) {
@@ -299,18 +311,18 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
             valid = pos >= 0 && pos < n;
           }
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
+          for (int j = 0; j < 8; ++j)
             sS[row * (HB + 1) + c0 + j] = valid ? __uint_as_float(r[j]) * sHead[c0 + j] : -INFINITY;
         }
       }
       tc_fence_before();
-      named_bar(1, 128);
+      named_bar(1, kSmThreads);
       if (tid == 0) mbar_arrive(&s_free[i & 1]);
       // 2. per-head tile max
       float mx = -INFINITY;
       for (int j = part; j < kTile; j += QN) mx = fmaxf(mx, sS[j * (HB + 1) + hh]);
       sRed[part * HB + hh] = mx;
-      named_bar(1, 128);
+      named_bar(1, kSmThreads);
       if (tid < HB) {
         float m = -INFINITY;
         for (int q = 0; q < QN; ++q) m = fmaxf(m, sRed[q * HB + tid]);
@@ -324,12 +336,13 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
         }
         sHead[3 * HB + tid] = alpha;
       }
-      named_bar(1, 128);
+      named_bar(1, kSmThreads);
       // 3. P = 2^(x - m) -> e4m3 (<= 256); partial sums of the quantized P
       const float m = sHead[HB + hh];
       float lsum = 0.f;
-      // the previous MMA2 must have finished reading sP (and writing O^T)
-      if (i >= 1 && !mbar_wait(o_done, (i - 1) & 1, p.err)) { ok = false; }
+      // P^T buffer (i % kPB) was last read by MMA2 of tile i - kPB
+      if (i >= S::kPB && !mbar_wait(&o_done[(i - S::kPB) & 1], ((i - S::kPB) >> 1) & 1, p.err)) { ok = false; }
+      uint8_t* sPi = sP + (i % S::kPB) * S::kPPad;
       for (int j = part; j < kTile; j += QN) {
         const float x = sS[j * (HB + 1) + hh];
         const float pv = (x == -INFINITY) ? 0.f : exp2f(x - m);
@@ -339,23 +352,24 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
         f8.__x = qb;
         lsum += float(f8);
         // MN-major no-swizzle core-matrix layout: [k group j/8][n chunk h/16][8 x 16]
-        sP[(j >> 3) * (HB / 16) * 128 + (hh >> 4) * 128 + (j & 7) * 16 + (hh & 15)] = qb;
+        sPi[(j >> 3) * (HB / 16) * 128 + (hh >> 4) * 128 + (j & 7) * 16 + (hh & 15)] = qb;
       }
-      sRed[128 + part * HB + hh] = lsum;
-      named_bar(1, 128);
+      sRed[kSmThreads + part * HB + hh] = lsum;
+      named_bar(1, kSmThreads);
       if (tid < HB) {
         float l = 0.f;
-        for (int q = 0; q < QN; ++q) l += sRed[128 + q * HB + tid];
+        for (int q = 0; q < QN; ++q) l += sRed[kSmThreads + q * HB + tid];
         sHead[2 * HB + tid] = sHead[2 * HB + tid] * sHead[3 * HB + tid] + l;
       }
-      // 4. rescale O^T columns whose max moved (rare)
+      // 4. rescale O^T columns whose max moved (rare): after MMA2 of tile i - 1
       if (sFlag[0] && i >= 1) {
+        if (!mbar_wait(&o_done[(i - 1) & 1], ((i - 1) >> 1) & 1, p.err)) ok = false;
         tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           const uint32_t ob = tmem + S::kTmemO + c * HB + (uint32_t(sub * 32) << 16);
 #pragma unroll
-          for (int c0 = 0; c0 < HB; c0 += 8) {
+          for (int c0 = hc0; c0 < hc0 + HB / 2; c0 += 8) {
             uint32_t r[8];
             tmem_ld_x8(ob + c0, r);
             tmem_ld_wait();
@@ -368,22 +382,22 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      named_bar(1, 128);
+      named_bar(1, kSmThreads);
       if (tid == 0) {
         sFlag[0] = 0;
-        mbar_arrive(p_full);
+        mbar_arrive(&p_full[i & 1]);
       }
       if (!ok) break;
     }
     // 5. epilogue: O^T (lane = latent row within block c, column = head)
-    if (nt > 0 && ok && mbar_wait(o_done, (nt - 1) & 1, p.err)) {
+    if (nt > 0 && ok && mbar_wait(&o_done[(nt - 1) & 1], ((nt - 1) >> 1) & 1, p.err)) {
       tc_fence_after();
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         const uint32_t ob = tmem + S::kTmemO + c * HB + (uint32_t(sub * 32) << 16);
         const int d = c * 128 + row;
 #pragma unroll
-        for (int c0 = 0; c0 < HB; c0 += 8) {
+        for (int c0 = hc0; c0 < hc0 + HB / 2; c0 += 8) {
           uint32_t r[8];
           tmem_ld_x8(ob + c0, r);
           tmem_ld_wait();
@@ -411,7 +425,7 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
       p.part_lse[(int64_t)split * gridDim.x * p.H + (int64_t)t * p.H + h0 + tid] = -INFINITY;
     }
     if (nt == 0 && p.nsplit == 1) {
-      for (int e = tid; e < HB * kL; e += 128)
+      for (int e = tid; e < HB * kL; e += kSmThreads)
         p.out[((int64_t)t * p.H + h0) * kL + e] = __float2bfloat16(0.f);
     }
   }
@@ -555,16 +569,18 @@ int b200_mla_tc(const MlaTcArgs* a, cudaStream_t st) {
   using namespace b200::mla;
   if (a->T <= 0) return 0;
   if (a->page_size != kPage || a->nsplit < 1 || a->nsplit > 16) return -1;
+  const int hb = a->hb ? a->hb : (a->H % 64 == 0 ? 64 : a->H % 32 == 0 ? 32 : 16);
+  if (a->H % hb != 0) return -6;
   if (a->topk != nullptr) {
     if (a->topk_n <= 0) return -1;
-    if (a->H % 64 == 0) return launch<64, true>(*a, st);
-    if (a->H % 32 == 0) return launch<32, true>(*a, st);
-    if (a->H % 16 == 0) return launch<16, true>(*a, st);
+    if (hb == 64) return launch<64, true>(*a, st);
+    if (hb == 32) return launch<32, true>(*a, st);
+    if (hb == 16) return launch<16, true>(*a, st);
     return -6;
   }
-  if (a->H % 64 == 0) return launch<64, false>(*a, st);
-  if (a->H % 32 == 0) return launch<32, false>(*a, st);
-  if (a->H % 16 == 0) return launch<16, false>(*a, st);
+  if (hb == 64) return launch<64, false>(*a, st);
+  if (hb == 32) return launch<32, false>(*a, st);
+  if (hb == 16) return launch<16, false>(*a, st);
   return -6;
 }
 
