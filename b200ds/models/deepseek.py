@@ -165,14 +165,14 @@ class DeepseekModel:
                      self.kv_cache[i], fb.out_slots, self.kv_scale[i], c.kv_lora_rank)
         qo = aw.q_b(q_lat, out_dtype=torch.float32 if self.device.type == "cpu" else torch.bfloat16)
         q = qo[:, : self.heads * c.qk_head_dim].view(T, self.heads, c.qk_head_dim)
-        q_pe = ops.rope(q[..., c.qk_nope_head_dim:], fb.positions, self.rope_table)
         q_abs = ops.absorb_q(q[..., : c.qk_nope_head_dim], aw.w_uk)       # [T, Hl, kv_lora]
         topk = None
         if c.index_n_heads:
             topk = self._indexer(i, aw, qkv, qo, fb)
-        o_lat = ops.mla_attention(q_abs, q_pe, self.kv_cache[i], self.kv_scale[i], fb,
-                                  c.softmax_scale, self.page_size, topk)
-        o = ops.absorb_o(o_lat, aw.w_uv)                                  # [T, Hl*v]
+        # q's rope part goes in un-rotated: RoPE is fused into the attention's query prep
+        o_lat = ops.mla_attention(q_abs, q[..., c.qk_nope_head_dim:], self.kv_cache[i], self.kv_scale[i], fb,
+                                  c.softmax_scale, self.page_size, topk, rope_table=self.rope_table)
+        o = ops.absorb_o(o_lat, aw.w_uv, quantize=aw.o_proj.quantized)   # [T, Hl*v] (MXFP8 when quantized)
         if self.device.type == "cuda" and self.attn_tp > 1:
             # leave the o_proj GEMM to the all-reduce so it can run fused
             return ops.PendingLinear(o, aw.o_proj.w, aw.o_proj.out_features)

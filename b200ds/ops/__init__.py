@@ -252,17 +252,27 @@ def absorb_q(q_nope: torch.Tensor, w_uk: torch.Tensor) -> torch.Tensor:
     return torch.einsum("thd,hdc->thc", q_nope.float(), w_uk.float())
 
 
-def absorb_o(o_lat: torch.Tensor, w_uv: torch.Tensor) -> torch.Tensor:
-    """[T, H, L] x [H, v, L] -> [T, H*v]."""
+def absorb_o(o_lat: torch.Tensor, w_uv: torch.Tensor, quantize: bool = False):
+    """[T, H, L] x [H, v, L] -> [T, H*v].  With quantize=True on the native
+    path the result comes back as the MXFP8 operand of the output projection
+    (quantized straight from the head-major batched-GEMM output)."""
     T, H, L = o_lat.shape
     if o_lat.is_cuda:
-        return torch.bmm(o_lat.transpose(0, 1).to(w_uv.dtype), w_uv.transpose(1, 2)).transpose(0, 1).reshape(T, -1)
+        y = torch.bmm(o_lat.transpose(0, 1).to(w_uv.dtype), w_uv.transpose(1, 2))      # [H, T, v]
+        if quantize and _IMPL == "native":
+            return _native().quant_heads(y)
+        return y.transpose(0, 1).reshape(T, -1)
     return torch.einsum("thc,hdc->thd", o_lat.float(), w_uv.float()).reshape(T, -1)
 
 
-def mla_attention(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size, topk=None):
+def mla_attention(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size, topk=None, rope_table=None):
+    """Absorbed MLA.  With rope_table, q_pe is the un-rotated rope part and
+    RoPE is applied here (fused into the native kernel's query prep)."""
     if _use_native(q_abs):
-        return _native().mla_attention(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size, topk)
+        return _native().mla_attention(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size, topk,
+                                       rope_table=rope_table)
+    if rope_table is not None:
+        q_pe = ref.rope(q_pe, fb.positions, rope_table)
     out = ref.mla_attention(q_abs, q_pe, cache, kv_scale, fb.block_table, fb.seq_lens, fb.q_seq,
                             fb.positions, softmax_scale, page_size, topk)
     return out.to(q_abs.dtype) if q_abs.is_cuda else out

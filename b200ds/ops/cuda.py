@@ -205,21 +205,40 @@ def mla_splits(T: int, H: int, max_len: int) -> int:
     return max(1, min(16, 148 // max(ctas, 1), tiles // 2))
 
 
-def mla_attention(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size, topk=None, impl=None):
+def quant_heads(y: torch.Tensor):
+    """[H, T, v] bf16 (head-major batched-GEMM output) -> MXFP8 QAct [T, H*v]."""
+    H, T, v = y.shape
+    a = alloc_qact(T, H * v, y.device)
+    _C.quant_heads(y.contiguous(), a.q, a.sf)
+    return a
+
+
+def mla_attention(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size, topk=None, impl=None,
+                  rope_table=None):
     T, H, L = q_abs.shape
     dev = q_abs.device
     out = torch.empty(T, H, L, dtype=torch.bfloat16, device=dev)
-    qa = q_abs.to(torch.bfloat16).contiguous()
-    qp = q_pe.to(torch.bfloat16).contiguous()
     use_tc = (impl or "tc") == "tc" and page_size == 64 and L == 512 and H % 16 == 0 \
         and q_pe.shape[-1] == 64
     if not use_tc:
-        _C.mla_simt(qa, qp, cache.view(torch.uint8), kv_scale, fb.block_table, fb.q_seq, fb.positions, topk,
-                    page_size, softmax_scale, out)
+        qp = q_pe.to(torch.bfloat16).contiguous()
+        if rope_table is not None:
+            rope(qp, fb.positions, rope_table)
+        _C.mla_simt(q_abs.to(torch.bfloat16).contiguous(), qp, cache.view(torch.uint8), kv_scale, fb.block_table,
+                    fb.q_seq, fb.positions, topk, page_size, softmax_scale, out)
         return out
     q8 = torch.empty(T, H, 576, dtype=torch.uint8, device=dev)
     qs = torch.empty(T, H, dtype=torch.float32, device=dev)
-    _C.mla_q_quant(qa, qp, q8, qs)
+    if rope_table is not None and q_abs.dtype == torch.bfloat16 and q_pe.dtype == torch.bfloat16 \
+            and q_abs.stride(-1) == 1 and q_pe.stride(-1) == 1:
+        # RoPE + e4m3 straight from the strided projections (no copies)
+        _C.mla_q_prep(q_abs, q_pe, fb.positions, rope_table, q8, qs)
+    else:
+        qa = q_abs.to(torch.bfloat16).contiguous()
+        qp = q_pe.to(torch.bfloat16).contiguous()
+        if rope_table is not None:
+            rope(qp, fb.positions, rope_table)
+        _C.mla_q_quant(qa, qp, q8, qs)
     keys = int(fb.max_seq_len) if fb.max_seq_len else 4096
     if topk is not None:
         keys = min(keys, int(topk.shape[1]))

@@ -42,6 +42,10 @@ int b200_ix_score(const uint8_t* q8, const float* wq, int T, int NH, const uint8
 int b200_topk_select(const float* scores, int64_t ld, const int* q_pos, int T, int K, int* out, cudaStream_t st);
 
 int b200_mla_q_quant(const void* q_abs, const void* q_pe, int TH, uint8_t* q8, float* qs, cudaStream_t st);
+// RoPE of the un-rotated q_pe + e4m3 quantization of [q_abs | q_pe] from
+// strided bf16 inputs (token stride, head stride in elements).
+int b200_mla_q_prep(const void* q_abs, int64_t qa_t, int64_t qa_h, const void* q_pe, int64_t qp_t, int64_t qp_h, int T,
+                    int H, const int* pos, const float* table, uint8_t* q8, float* qs, cudaStream_t st);
 int b200_mla_tc(const MlaTcArgs* args, cudaStream_t st);
 
 // ---------------------------------------------------------------------------

@@ -41,6 +41,20 @@ void mla_q_quant(const at::Tensor& q_abs, const at::Tensor& q_pe, at::Tensor q8,
               "mla_q_quant failed");
 }
 
+void mla_q_prep(const at::Tensor& q_abs, const at::Tensor& q_pe, const at::Tensor& pos, const at::Tensor& table,
+                at::Tensor q8, at::Tensor qs) {
+  TORCH_CHECK(q_abs.is_cuda() && q_abs.dim() == 3 && q_abs.size(2) == 512 && q_abs.stride(2) == 1, "q_abs [T,H,512]");
+  TORCH_CHECK(q_pe.dim() == 3 && q_pe.size(2) == 64 && q_pe.stride(2) == 1, "q_pe [T,H,64]");
+  TORCH_CHECK(q_abs.scalar_type() == at::kBFloat16 && q_pe.scalar_type() == at::kBFloat16, "bf16");
+  TORCH_CHECK(table.size(1) == 64 && pos.scalar_type() == at::kInt, "rope table [P, 64], pos int32");
+  const c10::cuda::CUDAGuard g(q_abs.device());
+  const int rc = b200_mla_q_prep(q_abs.data_ptr(), q_abs.stride(0), q_abs.stride(1), q_pe.data_ptr(), q_pe.stride(0),
+                                 q_pe.stride(1), q_abs.size(0), q_abs.size(1), pos.data_ptr<int>(), table.data_ptr<float>(),
+                                 reinterpret_cast<uint8_t*>(q8.data_ptr()), qs.data_ptr<float>(),
+                                 at::cuda::getCurrentCUDAStream().stream());
+  TORCH_CHECK(rc == 0, "mla_q_prep failed ", rc);
+}
+
 void mla_tc(const at::Tensor& q8, const at::Tensor& qs, const at::Tensor& cache, double kv_scale,
             const at::Tensor& block_table, const at::Tensor& q_seq, const at::Tensor& q_pos, int64_t page_size,
             double sm_scale, int64_t nsplit, at::Tensor out, c10::optional<at::Tensor> part_o,
@@ -141,6 +155,7 @@ void topk_select(const at::Tensor& scores, const at::Tensor& q_pos, at::Tensor o
 void register_attn(pybind11::module& m) {
   m.def("mla_simt", &mla_simt);
   m.def("mla_q_quant", &mla_q_quant);
+  m.def("mla_q_prep", &mla_q_prep);
   m.def("mla_tc", &mla_tc, pybind11::arg("q8"), pybind11::arg("qs"), pybind11::arg("cache"), pybind11::arg("kv_scale"),
         pybind11::arg("block_table"), pybind11::arg("q_seq"), pybind11::arg("q_pos"), pybind11::arg("page_size"),
         pybind11::arg("sm_scale"), pybind11::arg("nsplit"), pybind11::arg("out"), pybind11::arg("part_o"),

@@ -489,6 +489,45 @@ __global__ void q_quant_kernel(const __nv_bfloat16* q_abs, const __nv_bfloat16* 
   if (lane == 0) qs[w] = sc;
 }
 
+// q_abs (strided [T,H,512] bf16, e.g. the head-major batched-GEMM output) and
+// the un-rotated rope part q_pe (strided [T,H,64]) -> RoPE on q_pe, then e4m3
+// [T,H,576] with a per-(t,h) fp32 scale: one warp per (token, head).
+__global__ void q_prep_kernel(const __nv_bfloat16* q_abs, int64_t qa_t, int64_t qa_h, const __nv_bfloat16* q_pe,
+                              int64_t qp_t, int64_t qp_h, int T, int H, const int* pos, const float* table,
+                              uint8_t* q8, float* qs) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  pdl_wait();
+  pdl_launch_dependents();   // dependents wait for this grid before touching its outputs
+  if (w >= T * H) return;
+  const int t = w / H, h = w - t * H;
+  const __nv_bfloat16* a = q_abs + (int64_t)t * qa_t + (int64_t)h * qa_h;
+  const __nv_bfloat16* r = q_pe + (int64_t)t * qp_t + (int64_t)h * qp_h;
+  float v[18];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __bfloat162float(a[lane + 32 * i]);
+  {
+    // rope pair (2 lane, 2 lane + 1) at frequency lane; table row = cos(32) | sin(32)
+    const float x0 = __bfloat162float(r[2 * lane]), x1 = __bfloat162float(r[2 * lane + 1]);
+    const float* tr = table + (int64_t)pos[t] * kR;
+    const float c = tr[lane], sn = tr[kR / 2 + lane];
+    v[16] = x0 * c - x1 * sn;
+    v[17] = x0 * sn + x1 * c;
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 18; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float sc = amax > 0.f ? amax / 448.f : 1.f;
+  const float inv = 1.f / sc;
+  uint8_t* dst = q8 + (int64_t)w * kD;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) dst[lane + 32 * i] = uint8_t(f2_to_e4m3x2(v[i] * inv, 0.f) & 0xFF);
+  *reinterpret_cast<uint16_t*>(dst + kL + 2 * lane) = f2_to_e4m3x2(v[16] * inv, v[17] * inv);
+  if (lane == 0) qs[w] = sc;
+}
+
 // ---------------------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -562,6 +601,15 @@ int b200_mla_q_quant(const void* q_abs, const void* q_pe, int TH, uint8_t* q8, f
   if (TH <= 0) return 0;
   b200::launch_pdl(b200::mla::q_quant_kernel, dim3((TH * 32 + 127) / 128), dim3(128), 0, st, 
       reinterpret_cast<const __nv_bfloat16*>(q_abs), reinterpret_cast<const __nv_bfloat16*>(q_pe), TH, q8, qs);
+  return cudaGetLastError() == cudaSuccess ? 0 : 1;
+}
+
+int b200_mla_q_prep(const void* q_abs, int64_t qa_t, int64_t qa_h, const void* q_pe, int64_t qp_t, int64_t qp_h, int T,
+                    int H, const int* pos, const float* table, uint8_t* q8, float* qs, cudaStream_t st) {
+  if (T * H <= 0) return 0;
+  b200::launch_pdl(b200::mla::q_prep_kernel, dim3((T * H * 32 + 127) / 128), dim3(128), 0, st,
+                   reinterpret_cast<const __nv_bfloat16*>(q_abs), qa_t, qa_h,
+                   reinterpret_cast<const __nv_bfloat16*>(q_pe), qp_t, qp_h, T, H, pos, table, q8, qs);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
 

@@ -57,6 +57,17 @@ void quant(const at::Tensor& x, at::Tensor q, at::Tensor sf) {
         "quant");
 }
 
+// x [H, T, v] (contiguous, head-major) -> MXFP8 rows [T, H * v].
+void quant_heads(const at::Tensor& x, at::Tensor q, at::Tensor sf) {
+  check_cuda(x, "x");
+  const c10::cuda::CUDAGuard g(x.device());
+  TORCH_CHECK(x.dim() == 3 && x.is_contiguous(), "x [H, T, v] contiguous");
+  const int H = x.size(0), T = x.size(1), v = x.size(2);
+  check(b200_quant_mxfp8_seg(x.data_ptr(), x.scalar_type() == at::kFloat, v, T, H * v, v, (int64_t)T * v,
+                             ptr<uint8_t>(q), ptr<uint8_t>(sf), cur_stream()),
+        "quant_heads");
+}
+
 void gemm(const at::Tensor& w, const at::Tensor& w_sf, int64_t w_sf_estride, const at::Tensor& x,
           const at::Tensor& x_sf, int64_t nw, int64_t t, int64_t k, int64_t epi, int64_t splits,
           c10::optional<at::Tensor> out, int64_t ldo, c10::optional<at::Tensor> q_out, c10::optional<at::Tensor> sf_out,
@@ -359,6 +370,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "b200ds native sm_100a kernels";
   m.def("rmsnorm", &rmsnorm);
   m.def("quant", &quant);
+  m.def("quant_heads", &quant_heads);
   m.def("gemm", &gemm);
   m.def("gemm_push", &gemm_push);
   m.def("rope", &rope);

@@ -38,3 +38,8 @@ int b200_lm_candidates(const void* logits, int f32, int64_t ld, int B, int n, in
 int b200_sample_final(const void* cand, int B, int Kc, int world, const ArPeers* peers, uint32_t* epoch,
                       uint32_t* ticket, const float* temperature, const float* top_p, const int* top_k,
                       const float* uniform, int64_t* tokens, uint32_t* err, cudaStream_t st);
+
+// MXFP8 quantization of rows gathered from head-major blocks: element k of
+// row r at x[r * ldx + (k / seg) * seg_stride + k % seg].
+int b200_quant_mxfp8_seg(const void* x, int x_is_f32, int ldx, int rows, int K, int seg, int64_t seg_stride,
+                         uint8_t* q, uint8_t* sf, cudaStream_t st);

@@ -153,17 +153,21 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const TX* __restrict_
 }
 
 // Plain MXFP8 quantization of x [rows, K] (bf16 or fp32).
+// Row k-th element at x[row * ldx + (k / seg) * seg_stride + k % seg]: seg = K
+// is a plain row-major matrix; seg < K gathers a row from head-major blocks
+// (e.g. [H, T, v] -> row t = concat over h), saving a transpose copy.
 template <typename TX>
-__global__ void __launch_bounds__(kThreads) quant_kernel(const TX* __restrict__ x, int ldx, int K, uint8_t* q,
-                                                         uint8_t* sf) {
+__global__ void __launch_bounds__(kThreads) quant_kernel(const TX* __restrict__ x, int ldx, int K, int seg,
+                                                         int64_t seg_stride, uint8_t* q, uint8_t* sf) {
   const int row = blockIdx.y;
   const int u = blockIdx.x * kThreads + threadIdx.x;
   const int units = K >> 3;
   pdl_wait();
   pdl_launch_dependents();   // dependents wait for this grid before touching its outputs
   float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  if (u < units) load8<TX>(x + (int64_t)row * ldx + u * 8, v);
-  quant8(v, q + (int64_t)row * K + u * 8, sf, row, u * 8, K >> 5, u < units);
+  const int k = u * 8;
+  if (u < units) load8<TX>(x + (int64_t)row * ldx + (int64_t)(k / seg) * seg_stride + k % seg, v);
+  quant8(v, q + (int64_t)row * K + k, sf, row, k, K >> 5, u < units);
 }
 
 }  // namespace ew
@@ -189,13 +193,20 @@ int b200_rmsnorm(const void* x, int x_is_f32, int ldx, float* residual, const fl
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
 
-int b200_quant_mxfp8(const void* x, int x_is_f32, int ldx, int rows, int K, uint8_t* q, uint8_t* sf,
-                     cudaStream_t st) {
-  if (K % 128 != 0 || rows <= 0) return -1;
+int b200_quant_mxfp8_seg(const void* x, int x_is_f32, int ldx, int rows, int K, int seg, int64_t seg_stride,
+                         uint8_t* q, uint8_t* sf, cudaStream_t st) {
+  if (K % 128 != 0 || rows <= 0 || seg % 8 != 0 || K % seg != 0) return -1;
   dim3 grid((K / 8 + kThreads - 1) / kThreads, rows), block(kThreads);
   if (x_is_f32)
-    b200::launch_pdl(quant_kernel<float>, dim3(grid), dim3(block), 0, st, reinterpret_cast<const float*>(x), ldx, K, q, sf);
+    b200::launch_pdl(quant_kernel<float>, dim3(grid), dim3(block), 0, st, reinterpret_cast<const float*>(x), ldx, K,
+                     seg, seg_stride, q, sf);
   else
-    b200::launch_pdl(quant_kernel<__nv_bfloat16>, dim3(grid), dim3(block), 0, st, reinterpret_cast<const __nv_bfloat16*>(x), ldx, K, q, sf);
+    b200::launch_pdl(quant_kernel<__nv_bfloat16>, dim3(grid), dim3(block), 0, st,
+                     reinterpret_cast<const __nv_bfloat16*>(x), ldx, K, seg, seg_stride, q, sf);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
+}
+
+int b200_quant_mxfp8(const void* x, int x_is_f32, int ldx, int rows, int K, uint8_t* q, uint8_t* sf,
+                     cudaStream_t st) {
+  return b200_quant_mxfp8_seg(x, x_is_f32, ldx, rows, K, K, 0, q, sf, st);
 }

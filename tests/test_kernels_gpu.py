@@ -591,3 +591,44 @@ def test_moe_fused_matches_two_launch(fp4, tiled, T, skew):
     torch.cuda.synchronize()
     cuda.check_device_errors()
     assert torch.equal(a, b) and torch.equal(b, c)
+
+
+def test_mla_fused_rope_query_prep():
+    """RoPE fused into the attention's query prep, reading q_abs / q_pe as
+    strided views (head-major batched-GEMM output, rope slice of q_b)."""
+    from types import SimpleNamespace
+    from b200ds.config import small_gpu_config
+    from b200ds.models.rope import cos_sin_table
+    from b200ds.ops import cuda, ref
+    torch.manual_seed(4)
+    H, L, R, ps = 16, 512, 64, 64
+    lens = [300, 77, 1000]
+    B = len(lens)
+    bt, rows = _paged(lens)
+    cache = (torch.randn(rows, L + R) * 0.5).to(torch.float8_e4m3fn)
+    table = cos_sin_table(small_gpu_config(), 2048)
+    q_seq = torch.arange(B, dtype=torch.int32)
+    q_pos = torch.tensor([n - 1 for n in lens], dtype=torch.int32)
+    qo = (torch.randn(B, H * 192 + 64) * 0.3).to(torch.bfloat16)        # q_b output (+ extra columns)
+    q = qo[:, : H * 192].view(B, H, 192)
+    q_abs_hm = (torch.randn(H, B, L) * 0.3).to(torch.bfloat16)           # head-major [H, T, L]
+    fb = SimpleNamespace(block_table=bt.to(DEV), q_seq=q_seq.to(DEV), positions=q_pos.to(DEV), is_decode=True,
+                         max_seq_len=max(lens))
+    qd = qo.to(DEV)[:, : H * 192].view(B, H, 192)
+    got = cuda.mla_attention(q_abs_hm.to(DEV).transpose(0, 1), qd[..., 128:], cache.to(DEV), 0.7, fb, 0.0625, ps,
+                             rope_table=table.to(DEV))
+    q_pe = ref.rope(q[..., 128:].float(), q_pos, table)
+    exp = ref.mla_attention(q_abs_hm.transpose(0, 1).float(), q_pe, cache, 0.7, bt, torch.tensor(lens), q_seq,
+                            q_pos, 0.0625, ps)
+    assert rel_err(got.cpu(), exp) < 3e-2
+
+
+def test_quant_heads_matches_transpose():
+    from b200ds.ops import cuda
+    y = torch.randn(16, 37, 128, device=DEV).to(torch.bfloat16)
+    a = cuda.quant_heads(y)
+    b = cuda.quant(y.transpose(0, 1).reshape(37, -1).contiguous())
+    from b200ds.ops.quant import unpack_sf
+    assert torch.equal(a.q.view(torch.uint8), b.q.view(torch.uint8))
+    # scale rows past T are padding of the 128-row chunks (never read)
+    assert torch.equal(unpack_sf(a.sf, 37, 2048), unpack_sf(b.sf, 37, 2048))
