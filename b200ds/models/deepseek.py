@@ -64,6 +64,7 @@ class AttnWeights:
     w_uk: torch.Tensor            # [Hl, nope, kv_lora]
     w_uv: torch.Tensor            # [Hl, v, kv_lora]
     o_proj: Linear                # [h, Hl * v]
+    w_uk_t: Optional[torch.Tensor] = None   # [Hl, kv_lora, nope] (GPU serving copy of w_uk)
     # Sparse indexer (optional).  Its projections ride on the attention GEMMs:
     # qkv_a has [wk (index_head_dim); weights_proj (index_n_heads)] appended
     # after the q_lora + kv rows, and q_b has the indexer's wq_b rows appended
@@ -115,6 +116,11 @@ class DeepseekModel:
         self.ix_cache: List[torch.Tensor] = []
         self.ix_scale: List[torch.Tensor] = []
         self.page_size = ecfg.page_size
+        if self.device.type == "cuda":
+            for lw in layers:       # [H, L, nope] copy of W_uk for the tensor-core absorption
+                w = lw.attn.w_uk
+                if w.dtype == torch.bfloat16 and getattr(lw.attn, "w_uk_t", None) is None:
+                    lw.attn.w_uk_t = w.transpose(1, 2).contiguous()
         # DP attention: each rank serves its own requests with replicated
         # attention / dense / shared-expert / LM-head weights (tp_size 1);
         # only the routed experts are split (EP) and exchanged at the MoE
@@ -165,13 +171,14 @@ class DeepseekModel:
                      self.kv_cache[i], fb.out_slots, self.kv_scale[i], c.kv_lora_rank)
         qo = aw.q_b(q_lat, out_dtype=torch.float32 if self.device.type == "cpu" else torch.bfloat16)
         q = qo[:, : self.heads * c.qk_head_dim].view(T, self.heads, c.qk_head_dim)
-        q_abs = ops.absorb_q(q[..., : c.qk_nope_head_dim], aw.w_uk)       # [T, Hl, kv_lora]
         topk = None
         if c.index_n_heads:
             topk = self._indexer(i, aw, qkv, qo, fb)
-        # q's rope part goes in un-rotated: RoPE is fused into the attention's query prep
-        o_lat = ops.mla_attention(q_abs, q[..., c.qk_nope_head_dim:], self.kv_cache[i], self.kv_scale[i], fb,
-                                  c.softmax_scale, self.page_size, topk, rope_table=self.rope_table)
+        # absorption of q_nope into the latent space, RoPE of the (un-rotated)
+        # rope part and the e4m3 query prep run fused ahead of the attention
+        o_lat = ops.mla_from_q(q[..., : c.qk_nope_head_dim], q[..., c.qk_nope_head_dim:], aw.w_uk,
+                               getattr(aw, "w_uk_t", None), self.kv_cache[i], self.kv_scale[i], fb,
+                               c.softmax_scale, self.page_size, topk, self.rope_table)
         o = ops.absorb_o(o_lat, aw.w_uv, quantize=aw.o_proj.quantized)   # [T, Hl*v] (MXFP8 when quantized)
         if self.device.type == "cuda" and self.attn_tp > 1:
             # leave the o_proj GEMM to the all-reduce so it can run fused

@@ -258,11 +258,26 @@ def absorb_o(o_lat: torch.Tensor, w_uv: torch.Tensor, quantize: bool = False):
     (quantized straight from the head-major batched-GEMM output)."""
     T, H, L = o_lat.shape
     if o_lat.is_cuda:
+        if (quantize and _IMPL == "native" and w_uv.dtype == torch.bfloat16 and w_uv.shape[1] == 128
+                and o_lat.dtype == torch.bfloat16):
+            return _native().absorb_o_mx(o_lat, w_uv.contiguous())
         y = torch.bmm(o_lat.transpose(0, 1).to(w_uv.dtype), w_uv.transpose(1, 2))      # [H, T, v]
         if quantize and _IMPL == "native":
             return _native().quant_heads(y)
         return y.transpose(0, 1).reshape(T, -1)
     return torch.einsum("thc,hdc->thd", o_lat.float(), w_uv.float()).reshape(T, -1)
+
+
+def mla_from_q(q_nope, q_pe, w_uk, w_uk_t, cache, kv_scale, fb, softmax_scale, page_size, topk, rope_table):
+    """Absorbed MLA from the projected query: q_nope [T,H,nope] is absorbed
+    into the latent space (w_uk [H,nope,L]; w_uk_t = its [H,L,nope] copy used
+    by the fused tensor-core kernel), q_pe [T,H,rope] is rotated here."""
+    if (_use_native(q_nope) and w_uk_t is not None and q_nope.dtype == torch.bfloat16 and page_size == 64
+            and w_uk_t.shape[1] == 512 and q_nope.shape[1] % 16 == 0 and q_pe.shape[-1] == 64):
+        return _native().mla_decode_from_q(q_nope, q_pe, w_uk_t, cache, kv_scale, fb, softmax_scale, page_size,
+                                           topk, rope_table)
+    q_abs = absorb_q(q_nope, w_uk)
+    return mla_attention(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size, topk, rope_table=rope_table)
 
 
 def mla_attention(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size, topk=None, rope_table=None):

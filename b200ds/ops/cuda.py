@@ -213,14 +213,41 @@ def quant_heads(y: torch.Tensor):
     return a
 
 
+def absorb_q_prep(q_nope, q_pe, w_uk_t, pos, table):
+    """tcgen05 absorption of the query into the latent space fused with RoPE
+    and e4m3 quantization: q_nope / q_pe strided [T, H, 128 / 64] bf16 views,
+    w_uk_t [H, 512, 128] -> (q8 [T, H, 576] e4m3, qs [T, H])."""
+    T, H, _ = q_nope.shape
+    q8 = torch.empty(T, H, 576, dtype=torch.uint8, device=q_nope.device)
+    qs = torch.empty(T, H, dtype=torch.float32, device=q_nope.device)
+    _C.bf16_absorb(w_uk_t, q_nope, 1, None, q_pe, pos, table, q8, qs, None, None)
+    return q8, qs
+
+
+def absorb_o_mx(o_lat, w_uv):
+    """tcgen05 value absorption [T, H, 512] x [H, 128, 512] fused with the
+    MXFP8 quantization of the output projection's operand [T, H * 128]."""
+    T, H, _ = o_lat.shape
+    a = alloc_qact(T, H * w_uv.shape[1], o_lat.device)
+    _C.bf16_absorb(w_uv, o_lat, 2, None, None, None, None, None, None, a.q, a.sf)
+    return a
+
+
+def mla_decode_from_q(q_nope, q_pe, w_uk_t, cache, kv_scale, fb, softmax_scale, page_size, topk, rope_table):
+    """Absorbed MLA from the un-absorbed query: absorption + RoPE + quant in one
+    tcgen05 kernel, then the attention kernel (+ split merge)."""
+    q8, qs = absorb_q_prep(q_nope, q_pe, w_uk_t, fb.positions, rope_table)
+    return _mla_core(q8, qs, cache, kv_scale, fb, softmax_scale, page_size, topk)
+
+
 def mla_attention(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size, topk=None, impl=None,
                   rope_table=None):
     T, H, L = q_abs.shape
     dev = q_abs.device
-    out = torch.empty(T, H, L, dtype=torch.bfloat16, device=dev)
     use_tc = (impl or "tc") == "tc" and page_size == 64 and L == 512 and H % 16 == 0 \
         and q_pe.shape[-1] == 64
     if not use_tc:
+        out = torch.empty(T, H, L, dtype=torch.bfloat16, device=dev)
         qp = q_pe.to(torch.bfloat16).contiguous()
         if rope_table is not None:
             rope(qp, fb.positions, rope_table)
@@ -239,6 +266,14 @@ def mla_attention(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size, to
         if rope_table is not None:
             rope(qp, fb.positions, rope_table)
         _C.mla_q_quant(qa, qp, q8, qs)
+    return _mla_core(q8, qs, cache, kv_scale, fb, softmax_scale, page_size, topk)
+
+
+def _mla_core(q8, qs, cache, kv_scale, fb, softmax_scale, page_size, topk):
+    T, H, _ = q8.shape
+    L = 512
+    dev = q8.device
+    out = torch.empty(T, H, L, dtype=torch.bfloat16, device=dev)
     keys = int(fb.max_seq_len) if fb.max_seq_len else 4096
     if topk is not None:
         keys = min(keys, int(topk.shape[1]))

@@ -57,6 +57,46 @@ void quant(const at::Tensor& x, at::Tensor q, at::Tensor sf) {
         "quant");
 }
 
+// Batched bf16 GEMM for the MLA absorptions (csrc/gemm/gemm_bf16.cu).
+//   x: [T, B, K] view (unit inner stride), w: [B, M, K] contiguous bf16.
+void bf16_absorb(const at::Tensor& w, const at::Tensor& x, int64_t epi, c10::optional<at::Tensor> out,
+                 c10::optional<at::Tensor> q_pe, c10::optional<at::Tensor> pos, c10::optional<at::Tensor> table,
+                 c10::optional<at::Tensor> q8, c10::optional<at::Tensor> qs, c10::optional<at::Tensor> q,
+                 c10::optional<at::Tensor> sf) {
+  check_cuda(w, "w");
+  const c10::cuda::CUDAGuard g(w.device());
+  TORCH_CHECK(w.dim() == 3 && w.is_contiguous() && w.scalar_type() == at::kBFloat16, "w bf16 [B, M, K]");
+  TORCH_CHECK(x.dim() == 3 && x.stride(2) == 1 && x.scalar_type() == at::kBFloat16, "x bf16 [T, B, K]");
+  Bf16GemmArgs a{};
+  a.w = w.data_ptr();
+  a.x = x.data_ptr();
+  a.x_ts = x.stride(0);
+  a.x_bs = x.stride(1);
+  a.T = x.size(0);
+  a.B = x.size(1);
+  a.K = x.size(2);
+  a.M = w.size(1);
+  TORCH_CHECK(w.size(0) == a.B && w.size(2) == a.K, "shapes");
+  a.epi = epi;
+  if (out.has_value()) {
+    a.out = out->data_ptr();
+    a.out_ts = out->stride(0);
+    a.out_bs = out->stride(1);
+  }
+  if (q_pe.has_value()) {
+    a.q_pe = q_pe->data_ptr();
+    a.pe_ts = q_pe->stride(0);
+    a.pe_bs = q_pe->stride(1);
+  }
+  a.pos = optr<int>(pos);
+  a.table = optr<float>(table);
+  a.q8 = optr<uint8_t>(q8);
+  a.qs = optr<float>(qs);
+  a.q = optr<uint8_t>(q);
+  a.sf = optr<uint8_t>(sf);
+  check(b200_bf16_gemm(&a, cur_stream()), "bf16_absorb");
+}
+
 // x [H, T, v] (contiguous, head-major) -> MXFP8 rows [T, H * v].
 void quant_heads(const at::Tensor& x, at::Tensor q, at::Tensor sf) {
   check_cuda(x, "x");
@@ -371,6 +411,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm", &rmsnorm);
   m.def("quant", &quant);
   m.def("quant_heads", &quant_heads);
+  m.def("bf16_absorb", &bf16_absorb);
   m.def("gemm", &gemm);
   m.def("gemm_push", &gemm_push);
   m.def("rope", &rope);

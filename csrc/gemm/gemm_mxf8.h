@@ -123,3 +123,24 @@ struct MoeFusedArgs {
   float out_g;             // NVFP4: global scale of the FC1 output
 };
 int b200_moe_fused(const MoeFusedArgs* args, cudaStream_t stream);
+
+// Batched bf16 swap-AB GEMM for the MLA weight absorptions (see gemm_bf16.cu).
+struct Bf16GemmArgs {
+  const void* w;           // bf16 [B][M][K] (K contiguous)
+  const void* x;           // bf16 tokens: element (t, b, k) at x[t * x_ts + b * x_bs + k]
+  int64_t x_ts, x_bs;
+  int T, K, M, B;
+  int epi;                 // 0 bf16 store, 1 absorb_q + query prep, 2 absorb_o + MXFP8 rows
+  void* out;               // epi 0: bf16, element (t, b, m) at out[t * out_ts + b * out_bs + m]
+  int64_t out_ts, out_bs;
+  const void* q_pe;        // epi 1: un-rotated rope part, (t, b, d) at q_pe[t * pe_ts + b * pe_bs + d]
+  int64_t pe_ts, pe_bs;
+  const int* pos;
+  const float* table;
+  uint8_t* q8;             // epi 1: e4m3 [T, B, 576]
+  float* qs;               // epi 1: [T, B]
+  uint8_t* q;              // epi 2: e4m3 [T, B * 128]
+  uint8_t* sf;             // epi 2: scales (tcgen05 layout, K = B * 128)
+  uint32_t* err;
+};
+int b200_bf16_gemm(const Bf16GemmArgs* args, cudaStream_t stream);

@@ -632,3 +632,37 @@ def test_quant_heads_matches_transpose():
     assert torch.equal(a.q.view(torch.uint8), b.q.view(torch.uint8))
     # scale rows past T are padding of the 128-row chunks (never read)
     assert torch.equal(unpack_sf(a.sf, 37, 2048), unpack_sf(b.sf, 37, 2048))
+
+
+@pytest.mark.parametrize("T,H", [(64, 16), (5, 32), (130, 16)])
+def test_absorb_q_fused_query_prep(T, H):
+    """tcgen05 bf16 absorption of q_nope into the latent, fused with RoPE and
+    the e4m3 query prep, vs fp32 math (dequantized output)."""
+    from b200ds.config import small_gpu_config
+    from b200ds.models.rope import cos_sin_table
+    from b200ds.ops import cuda, ref
+    torch.manual_seed(5)
+    table = cos_sin_table(small_gpu_config(), 4096).to(DEV)
+    qo = (torch.randn(T, H * 192 + 64, device=DEV) * 0.5).to(torch.bfloat16)
+    q = qo[:, : H * 192].view(T, H, 192)
+    w_uk = (torch.randn(H, 128, 512, device=DEV) * 0.05).to(torch.bfloat16)
+    pos = torch.randint(0, 4000, (T,), dtype=torch.int32, device=DEV)
+    q8, qs = cuda.absorb_q_prep(q[..., :128], q[..., 128:], w_uk.transpose(1, 2).contiguous(), pos, table)
+    got = q8.view(torch.float8_e4m3fn).float() * qs.unsqueeze(-1)
+    lat = torch.einsum("thd,hdc->thc", q[..., :128].float(), w_uk.float())
+    pe = ref.rope(q[..., 128:].float(), pos, table)
+    exp = torch.cat([lat, pe], -1)
+    assert rel_err(got, exp) < 4e-2
+
+
+@pytest.mark.parametrize("T,H", [(64, 16), (7, 128)])
+def test_absorb_o_mxfp8_rows(T, H):
+    from b200ds.ops import cuda
+    from b200ds.ops.quant import dequant_mxfp8
+    torch.manual_seed(6)
+    o_lat = (torch.randn(T, H, 512, device=DEV) * 0.5).to(torch.bfloat16)
+    w_uv = (torch.randn(H, 128, 512, device=DEV) * 0.05).to(torch.bfloat16)
+    a = cuda.absorb_o_mx(o_lat, w_uv)
+    got = dequant_mxfp8(a.q, a.sf)[:T]
+    exp = torch.einsum("thc,hdc->thd", o_lat.float(), w_uv.float()).reshape(T, -1)
+    assert rel_err(got, exp) < 4e-2
