@@ -299,8 +299,17 @@ def router(x: torch.Tensor, gate: torch.Tensor, bias: torch.Tensor, cfg):
     if g16 is None or g16.shape != gate.shape:
         g16 = gate.to(torch.bfloat16).contiguous()
         _GATE_BF16[gate.data_ptr()] = g16
-    logits = torch.mm(x.to(torch.bfloat16), g16.t(), out_dtype=torch.float32)
-    T = logits.shape[0]
+    xb = x.to(torch.bfloat16)
+    T = xb.shape[0]
+    E, Kd = g16.shape
+    if E % 128 == 0 and Kd % 64 == 0 and xb.stride(-1) == 1:
+        # tcgen05 split-K GEMM (fp32 accumulate across splits)
+        logits = torch.zeros(T, E, dtype=torch.float32, device=x.device)
+        splits = max(1, min(32, (Kd // 64) // 4, 148 // max(1, (E // 128) * -(-T // 128))))
+        _C.bf16_absorb(g16.view(1, E, Kd), xb.view(T, 1, Kd), 3, logits.view(T, 1, E), None, None, None, None,
+                       None, None, None, splits=splits)
+    else:
+        logits = torch.mm(xb, g16.t(), out_dtype=torch.float32)
     K = cfg.num_experts_per_tok
     w = torch.empty(T, K, dtype=torch.float32, device=x.device)
     ids = torch.empty(T, K, dtype=torch.int32, device=x.device)

@@ -62,7 +62,7 @@ void quant(const at::Tensor& x, at::Tensor q, at::Tensor sf) {
 void bf16_absorb(const at::Tensor& w, const at::Tensor& x, int64_t epi, c10::optional<at::Tensor> out,
                  c10::optional<at::Tensor> q_pe, c10::optional<at::Tensor> pos, c10::optional<at::Tensor> table,
                  c10::optional<at::Tensor> q8, c10::optional<at::Tensor> qs, c10::optional<at::Tensor> q,
-                 c10::optional<at::Tensor> sf) {
+                 c10::optional<at::Tensor> sf, int64_t splits) {
   check_cuda(w, "w");
   const c10::cuda::CUDAGuard g(w.device());
   TORCH_CHECK(w.dim() == 3 && w.is_contiguous() && w.scalar_type() == at::kBFloat16, "w bf16 [B, M, K]");
@@ -78,6 +78,7 @@ void bf16_absorb(const at::Tensor& w, const at::Tensor& x, int64_t epi, c10::opt
   a.M = w.size(1);
   TORCH_CHECK(w.size(0) == a.B && w.size(2) == a.K, "shapes");
   a.epi = epi;
+  a.splits = splits;
   if (out.has_value()) {
     a.out = out->data_ptr();
     a.out_ts = out->stride(0);
@@ -411,7 +412,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm", &rmsnorm);
   m.def("quant", &quant);
   m.def("quant_heads", &quant_heads);
-  m.def("bf16_absorb", &bf16_absorb);
+  m.def("bf16_absorb", &bf16_absorb, pybind11::arg("w"), pybind11::arg("x"), pybind11::arg("epi"),
+        pybind11::arg("out"), pybind11::arg("q_pe"), pybind11::arg("pos"), pybind11::arg("table"),
+        pybind11::arg("q8"), pybind11::arg("qs"), pybind11::arg("q"), pybind11::arg("sf"),
+        pybind11::arg("splits") = 1);
   m.def("gemm", &gemm);
   m.def("gemm_push", &gemm_push);
   m.def("rope", &rope);

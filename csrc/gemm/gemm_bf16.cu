@@ -33,7 +33,7 @@ constexpr int kTileM = 128;
 constexpr int kTileKB = 128;      // bytes of K per stage (64 bf16)
 constexpr int kStages = 4;
 
-enum : int { kBf16Store = 0, kQPrep = 1, kMxfp8Rows = 2 };
+enum : int { kBf16Store = 0, kQPrep = 1, kMxfp8Rows = 2, kF32Atomic = 3 };
 
 template <int BN, int MT>
 struct Cfg {
@@ -63,6 +63,9 @@ struct Params {
   // kMxfp8Rows
   uint8_t* q;                // e4m3 [T, B * 128]
   uint8_t* sf;               // tcgen05 scale layout, K = B * 128
+  // kF32Atomic (split-K): out_f32[t * ot + m] += partial over this CTA's k-range
+  float* out_f32;
+  int splits;
   uint32_t* err;
 };
 
@@ -90,8 +93,12 @@ bf16_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
   const int warp = warp_id(), lane = lane_id();
   const int b = blockIdx.x;               // batch (head)
   const int t0 = blockIdx.y * BN;         // first token
-  const int m0 = blockIdx.z * MT;         // first 128-row tile
-  const int nk = p.K * 2 / kTileKB;
+  const int split = blockIdx.z % p.splits;
+  const int m0 = (blockIdx.z / p.splits) * MT;   // first 128-row tile
+  const int nk_all = p.K * 2 / kTileKB;
+  const int nk_per = (nk_all + p.splits - 1) / p.splits;
+  const int k_lo = split * nk_per;
+  const int nk = max(0, min(nk_all, k_lo + nk_per) - k_lo);
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
@@ -123,9 +130,9 @@ bf16_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
         const int mt = i / nk, kt = i - mt * nk;
         if (i >= kStages && !mbar_wait(&empty[s], ((i / kStages) - 1) & 1, p.err)) break;
         mbar_arrive_expect_tx(&full[s], C::kStage);
-        tma_load_3d_hint(sA + s * C::kA, &tm_a, &full[s], kt * (kTileKB / 2), (m0 + mt) * kTileM, b, pol_w);
+        tma_load_3d_hint(sA + s * C::kA, &tm_a, &full[s], (k_lo + kt) * (kTileKB / 2), (m0 + mt) * kTileM, b, pol_w);
         if (i == 0) pdl_wait();
-        tma_load_3d(sB + s * C::kB, &tm_x, &full[s], kt * (kTileKB / 2), t0, b);
+        tma_load_3d(sB + s * C::kB, &tm_x, &full[s], (k_lo + kt) * (kTileKB / 2), t0, b);
       }
       if (iters == 0) pdl_wait();
     }
@@ -176,12 +183,27 @@ bf16_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
       }
       named_barrier(1, 128);
     }
-    const bool ok = mbar_wait(acc_full, 0, p.err);
+    const bool ok = iters > 0 && mbar_wait(acc_full, 0, p.err);
     tc_fence_after();
     if (ok) {
       const uint32_t lane_addr = tmem + (uint32_t(sub * 32) << 16);
       const int rl = sub * 32 + lane;              // row within a 128-row tile
-      if constexpr (EPI == kBf16Store) {
+      if constexpr (EPI == kF32Atomic) {
+#pragma unroll 1
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll 1
+          for (int c0 = 0; c0 < BN; c0 += 16) {
+            uint32_t r[16];
+            tmem_ld_x16(lane_addr + mt * BN + c0, r);
+            tmem_ld_wait();
+            const int m = (m0 + mt) * kTileM + rl;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int t = t0 + c0 + j;
+              if (t < p.T) atomicAdd(p.out_f32 + (int64_t)t * p.ot + (int64_t)b * p.ob + m, __uint_as_float(r[j]));
+            }
+          }
+      } else if constexpr (EPI == kBf16Store) {
 #pragma unroll 1
         for (int mt = 0; mt < MT; ++mt)
 #pragma unroll 1
@@ -306,7 +328,7 @@ static int launch(const Bf16GemmArgs& a, const Params& p, cudaStream_t st) {
   if (map3(&mx, a.x, a.K, a.T, a.B, a.x_ts, a.x_bs, BN)) return -3;
   auto kern = bf16_gemm_kernel<BN, MT, EPI>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
-  const dim3 grid(a.B, (a.T + BN - 1) / BN, a.M / kTileM / MT);
+  const dim3 grid(a.B, (a.T + BN - 1) / BN, a.M / kTileM / MT * p.splits);
   b200::launch_pdl(kern, grid, dim3(kThreads), C::kSmem, st, ma, mx, p);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
@@ -332,6 +354,8 @@ int b200_bf16_gemm(const Bf16GemmArgs* a, cudaStream_t st) {
   p.M = a->M;
   p.B = a->B;
   p.err = a->err;
+  p.splits = a->splits > 0 ? a->splits : 1;
+  if (a->epi != kF32Atomic && p.splits != 1) return -1;
   switch (a->epi) {
     case kBf16Store:
       p.out = reinterpret_cast<__nv_bfloat16*>(a->out);
@@ -348,6 +372,11 @@ int b200_bf16_gemm(const Bf16GemmArgs* a, cudaStream_t st) {
       p.q8 = a->q8;
       p.qs = a->qs;
       return launch_bn<kQPrep, 4>(*a, p, st);
+    case kF32Atomic:
+      p.out_f32 = reinterpret_cast<float*>(a->out);
+      p.ot = a->out_ts;
+      p.ob = a->out_bs;
+      return launch_bn<kF32Atomic, 1>(*a, p, st);
     case kMxfp8Rows:
       if (a->M != 128) return -1;
       p.q = a->q;

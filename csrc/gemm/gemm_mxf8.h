@@ -130,7 +130,9 @@ struct Bf16GemmArgs {
   const void* x;           // bf16 tokens: element (t, b, k) at x[t * x_ts + b * x_bs + k]
   int64_t x_ts, x_bs;
   int T, K, M, B;
-  int epi;                 // 0 bf16 store, 1 absorb_q + query prep, 2 absorb_o + MXFP8 rows
+  int epi;                 // 0 bf16 store, 1 absorb_q + query prep, 2 absorb_o + MXFP8 rows,
+                           // 3 split-K fp32 atomic accumulate into out (zeroed by the caller)
+  int splits;              // epi 3: K splits (grid z = M tiles * splits)
   void* out;               // epi 0: bf16, element (t, b, m) at out[t * out_ts + b * out_bs + m]
   int64_t out_ts, out_bs;
   const void* q_pe;        // epi 1: un-rotated rope part, (t, b, d) at q_pe[t * pe_ts + b * pe_bs + d]

@@ -666,3 +666,19 @@ def test_absorb_o_mxfp8_rows(T, H):
     got = dequant_mxfp8(a.q, a.sf)[:T]
     exp = torch.einsum("thc,hdc->thd", o_lat.float(), w_uv.float()).reshape(T, -1)
     assert rel_err(got, exp) < 4e-2
+
+
+@pytest.mark.parametrize("T", [1, 64, 300])
+def test_router_gemm_split_k(T):
+    """Router logits on the tcgen05 bf16 split-K GEMM (fp32 accumulation
+    across splits) vs fp32 math on the same bf16 operands."""
+    from b200ds import _C
+    torch.manual_seed(8)
+    E, K = 256, 7168
+    x = torch.randn(T, K, device=DEV).to(torch.bfloat16)
+    g = (torch.randn(E, K, device=DEV) * 0.02).to(torch.bfloat16)
+    out = torch.zeros(T, E, device=DEV)
+    _C.bf16_absorb(g.view(1, E, K), x.view(T, 1, K), 3, out.view(T, 1, E), None, None, None, None, None, None, None,
+                   splits=16)
+    exp = x.float() @ g.float().T
+    assert rel_err(out, exp) < 1e-3
