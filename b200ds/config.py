@@ -196,3 +196,5 @@ class EngineConfig:
     gemm_impl: str = "native"        # "native" (own tcgen05 kernels) or "torch" (baseline)
     seed: int = 0
     weight_sets: int = 0             # >0: cycle this many distinct layer weight sets (when the model exceeds HBM)
+    spec_ngram: int = 0              # >0: speculative decoding with n-gram (prompt lookup) drafts up to this n
+    spec_k: int = 4                  # draft tokens verified per step

@@ -154,6 +154,7 @@ class Engine:
     def step(self) -> List[Request]:
         """Run one scheduler step; returns requests that finished."""
         st = self.sched.next_step()
+        multi = None
         if self.dp:
             toks = self._dp_forward(st)
             if st is None:
@@ -161,8 +162,14 @@ class Engine:
         elif st is None:
             return []
         else:
-            toks = self._forward(st)
-        self.sched.commit(st)
+            multi = self._spec_decode(st) if (self.ecfg.spec_ngram > 0 and st.kind == "decode") else None
+            toks = None if multi is not None else self._forward(st)
+        if multi is None:
+            self.sched.commit(st)
+            multi = [[t] for t in toks]
+        else:
+            for r, new in zip(st.reqs, multi):     # newest token + accepted drafts are cached now
+                r.cached += len(new)
         self._check_device_errors()
         now = time.perf_counter()
         done = []
@@ -170,24 +177,76 @@ class Engine:
         if st.kind == "prefill":
             self.stats["prefill_tokens"] += sum(len(c) for c in st.chunks)
         else:
-            self.stats["decode_tokens"] += len(st.reqs)
-        for r, smp, t in zip(st.reqs, st.sample, toks):
+            self.stats["decode_tokens"] += sum(len(m) for m in multi)
+        for r, smp, new in zip(st.reqs, st.sample, multi):
             if not smp:
                 continue
-            r.output.append(int(t))
-            r.token_times.append(now)
-            if r.t_first is None:
-                r.t_first = now
-            p = r.params
-            if len(r.output) >= p.max_tokens:
-                r.finished, r.finish_reason = True, "length"
-            elif not p.ignore_eos and ((self.eos is not None and t == self.eos) or t in p.stop_token_ids):
-                r.finished, r.finish_reason = True, "stop"
-            if r.finished:
-                r.t_done = now
-                self.sched.finish(r)
-                done.append(r)
+            for t in new:
+                r.output.append(int(t))
+                r.token_times.append(now)
+                if r.t_first is None:
+                    r.t_first = now
+                p = r.params
+                if len(r.output) >= p.max_tokens:
+                    r.finished, r.finish_reason = True, "length"
+                elif not p.ignore_eos and ((self.eos is not None and t == self.eos) or t in p.stop_token_ids):
+                    r.finished, r.finish_reason = True, "stop"
+                if r.finished:
+                    r.t_done = now
+                    self.sched.finish(r)
+                    done.append(r)
+                    break
         return done
+
+    # ------------------------------------------------------------------
+    # Speculative decoding (greedy): n-gram drafts verified in one forward
+    def _ngram_draft(self, r: Request) -> List[int]:
+        """Up to spec_k tokens that followed the most recent earlier occurrence
+        of the context's last n tokens (n = spec_ngram .. 1)."""
+        ctx = r.all_tokens[: r.cached + 1]
+        k = self.ecfg.spec_k
+        for n in range(min(self.ecfg.spec_ngram, len(ctx) - 1), 0, -1):
+            pat = ctx[-n:]
+            for j in range(len(ctx) - n - 1, -1, -1):
+                if ctx[j:j + n] == pat:
+                    d = ctx[j + n: j + n + k]
+                    if d:
+                        return d
+        return []
+
+    def _spec_decode(self, st: Step) -> Optional[List[List[int]]]:
+        """Verify per-request drafts with one forward over [newest token + draft]
+        (logits at every position).  Returns the accepted tokens per request
+        (accepted draft prefix + the model's next token), or None when no
+        request has a draft (plain decode then)."""
+        if self.dp or not st.reqs or any(r.params.temperature > 0 for r in st.reqs):
+            return None
+        drafts = []
+        for r in st.reqs:
+            room = r.params.max_tokens - len(r.output) - 1
+            d = self._ngram_draft(r)[: max(0, room)]
+            if d and not self.sched._ensure_pages(r, r.cached + 1 + len(d)):
+                d = []
+            drafts.append(d)
+        if not any(drafts):
+            return None
+        seqs = [{"tokens": ch + d, "start": s, "pages": r.pages}
+                for r, ch, s, d in zip(st.reqs, st.chunks, st.starts, drafts)]
+        fb = build_batch(seqs, self.ecfg.page_size, device="cpu")
+        fb.last_idx = torch.arange(fb.num_tokens, dtype=torch.int64)     # logits at every position
+        fb = self._to_device(fb)
+        pred = self.model.forward(fb).argmax(-1).tolist()
+        out, off = [], 0
+        for r, d in zip(st.reqs, drafts):
+            p = pred[off: off + 1 + len(d)]
+            a = 0
+            while a < len(d) and p[a] == d[a]:
+                a += 1
+            out.append(d[:a] + [p[a]])
+            off += 1 + len(d)
+            self.stats["spec_proposed"] = self.stats.get("spec_proposed", 0) + len(d)
+            self.stats["spec_accepted"] = self.stats.get("spec_accepted", 0) + a
+        return out
 
     def _check_device_errors(self) -> None:
         """Every device-side wait in the fused collectives is bounded; a wait
