@@ -1,0 +1,125 @@
+"""Host-side serving components on CPU: page pool reference counting, radix
+prefix cache (match / insert / LRU eviction under locks), scheduler
+(chunked prefill, preemption by recompute, page accounting), and engine
+behaviours (prefix reuse gives identical tokens, stop tokens, sampling
+determinism per seed, DP-free single process)."""
+import pytest
+import torch
+
+from b200ds.engine.request import Request, SamplingParams
+from b200ds.engine.scheduler import Scheduler
+from b200ds.kv.pool import OutOfPages, PagePool
+from b200ds.kv.radix import RadixCache
+
+
+def test_page_pool_refcounts():
+    pool = PagePool(8, 4)
+    assert pool.num_free == 7                 # page 0 reserved
+    a = pool.alloc(3)
+    assert 0 not in a and pool.num_free == 4
+    pool.retain(a[:1])
+    pool.release(a)
+    assert pool.num_free == 6                 # a[0] still referenced once
+    pool.release(a[:1])
+    assert pool.num_free == 7
+    with pytest.raises(OutOfPages):
+        pool.alloc(8)
+    assert pool.pages_for(9) == 3
+
+
+def test_radix_match_insert_evict():
+    pool = PagePool(16, 2)
+    rc = RadixCache(pool)
+    toks = [1, 2, 3, 4, 5, 6]
+    pages = pool.alloc(3)
+    rc.insert(toks, pages)
+    pool.release(pages)                       # the tree keeps its own references
+    assert pool.num_free == 15 - 3
+    got, nodes = rc.match([1, 2, 3, 4, 9, 9])
+    assert got == pages[:2] and len(nodes) == 2
+    # locked nodes are not evicted; the unlocked leaf is
+    assert rc.evict(5) == 1
+    assert pool.num_free == 15 - 2
+    rc.unlock(nodes)
+    assert rc.evict(5) == 2
+    assert pool.num_free == 15 and rc.num_nodes == 0
+
+
+def _req(i, n, max_tokens=4):
+    return Request(i, list(range(100 * i, 100 * i + n)), SamplingParams(max_tokens=max_tokens))
+
+
+def test_scheduler_chunked_prefill_and_decode():
+    pool = PagePool(64, 4)
+    s = Scheduler(pool, max_num_seqs=4, max_prefill_tokens=10)
+    a, b = _req(1, 13), _req(2, 5)
+    s.add(a)
+    s.add(b)
+    st = s.next_step()
+    assert st.kind == "prefill" and [len(c) for c in st.chunks] == [10] and st.sample == [False]
+    s.commit(st)
+    st = s.next_step()                        # b (5, waited for budget) + the rest of a (3)
+    assert st.kind == "prefill" and st.reqs == [b, a] and [len(c) for c in st.chunks] == [5, 3]
+    assert st.sample == [True, True]
+    s.commit(st)
+    for r in (a, b):
+        r.output.append(7)
+    st = s.next_step()
+    assert st.kind == "decode" and sorted(st.starts) == [5, 13]
+    assert all(len(r.pages) * 4 >= r.cached + 1 for r in (a, b))
+
+
+def test_scheduler_preempts_when_pages_run_out():
+    pool = PagePool(5, 4)                     # 4 usable pages = 16 tokens
+    s = Scheduler(pool, max_num_seqs=4, max_prefill_tokens=64)
+    a, b = _req(1, 7), _req(2, 7)
+    s.add(a)
+    s.add(b)
+    s.commit(s.next_step())
+    for r in (a, b):
+        r.output.append(1)
+    st = s.next_step()
+    s.commit(st)
+    for r in (a, b):
+        r.output.append(1)
+    st = s.next_step()                        # a needs a 3rd page: b is preempted and re-queued
+    assert st.kind == "decode" and st.reqs == [a]
+    assert b.cached == 0 and b.pages == [] and s.waiting[0] is b
+
+
+def _engine(prefix_cache=True, **kw):
+    from b200ds import build_model_from
+    from b200ds.config import EngineConfig, tiny_config
+    from b200ds.engine.engine import Engine
+    from b200ds.models.reference import init_weights
+    cfg = tiny_config()
+    ecfg = EngineConfig(page_size=8, cuda_graphs=False, enable_prefix_cache=prefix_cache, **kw)
+    return Engine(build_model_from(cfg, ecfg, init_weights(cfg, 0), device="cpu"), ecfg), cfg
+
+
+def test_prefix_cache_reuse_is_transparent():
+    eng, cfg = _engine(True)
+    g = torch.Generator().manual_seed(4)
+    shared = torch.randint(0, cfg.vocab_size, (24,), generator=g).tolist()
+    p1 = shared + [5, 6, 7]
+    p2 = shared + [8, 9]
+    first = eng.generate([p1], SamplingParams(max_tokens=6))[0].token_ids
+    again = eng.generate([p1, p2], SamplingParams(max_tokens=6))
+    assert eng.radix.num_nodes > 0
+    ref_eng, _ = _engine(False)
+    ref = ref_eng.generate([p1, p2], SamplingParams(max_tokens=6))
+    assert again[0].token_ids == first == ref[0].token_ids
+    assert again[1].token_ids == ref[1].token_ids
+
+
+def test_stop_tokens_and_seeded_sampling():
+    eng, cfg = _engine(False)
+    prompt = list(range(10))
+    greedy = eng.generate([prompt], SamplingParams(max_tokens=8))[0].token_ids
+    stop = greedy[3]
+    out = eng.generate([prompt], SamplingParams(max_tokens=8, stop_token_ids=[stop]))[0]
+    assert out.finish_reason == "stop" and out.token_ids == greedy[: greedy.index(stop) + 1]
+    sp = SamplingParams(max_tokens=8, temperature=0.9, top_p=0.95, seed=123)
+    a = eng.generate([prompt], sp)[0].token_ids
+    b = eng.generate([prompt], sp)[0].token_ids
+    assert a == b
