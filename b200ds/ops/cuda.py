@@ -327,6 +327,17 @@ def moe_tile_n(rows_per_expert: float, cap: int) -> int:
 
 
 MOE_FUSED = os.environ.get("B200_MOE_FUSED", "1") != "0"
+# the fused kernel reads FC1 rows straight from the activations / dispatch
+# buffer (no expert-sorted copy); 0 keeps the separate gather for comparison
+MOE_PULL = os.environ.get("B200_MOE_PULL", "1") != "0"
+
+
+def _fused(bn1: int, bn2: int) -> bool:
+    return MOE_FUSED and bn1 == bn2
+
+
+def _pulls(bn1: int, bn2: int) -> bool:
+    return MOE_PULL and _fused(bn1, bn2)
 
 
 def _moe_ws(ex, dev) -> torch.Tensor:
@@ -352,19 +363,26 @@ def check_device_errors() -> None:
             raise RuntimeError(f"fused expert GEMM: in-kernel dependency wait timed out (code {v})")
 
 
-def _expert_gemms(ex, xq, xsf, xg, hq, hsf, y, Hd, bn1, bn2, seg_start, seg_count, tt1, tt2, row_weight, fp4):
+def _expert_gemms(ex, xq, xsf, xg, hq, hsf, y, Hd, bn1, bn2, seg_start, seg_count, tt1, tt2, row_weight, fp4,
+                  pull=None):
     """FC1 (SwiGLU + requant into hq) and FC2 (routing-weighted into y): one
     fused persistent launch when both use the same token tile (decode), else
-    two grouped launches."""
+    two grouped launches.  pull (fused only): dict of the FC1 row sources
+    (row_token, src_q / src_sf / src_g addresses, src_rows, optional
+    src_epoch / src_epoch_add / src_par_bytes) read in place of xq."""
     E, I = ex.count, ex.inter
     w13, w2 = ex.w13, ex.w2
     g2 = float(ex.fc2_act_scale)
-    if MOE_FUSED and bn1 == bn2:
+    if _fused(bn1, bn2):
         ws = _moe_ws(ex, y.device)
+        if pull is not None:
+            xq, xsf, xg = hq, hsf, None      # unused operands (rows come from the sources)
         _C.moe_fused(w13.data, w13.sf, w2.data, w2.sf, xq, xsf, hq, hsf, y, E, Hd, I, bn1, seg_start, seg_count, tt1,
                      row_weight, ws, ex._fused_err, 0, True, ex.tiled,
-                     xg if fp4 else None, w13.global_scale if fp4 else None, w2.global_scale if fp4 else None, g2)
+                     xg if fp4 else None, w13.global_scale if fp4 else None, w2.global_scale if fp4 else None, g2,
+                     **(pull or {}))
         return
+    assert pull is None, "pulled rows need the fused expert kernel"
     if fp4:
         _C.gemm_grouped(w13.data, w13.sf, xq, xsf, 2 * I, Hd, E, I, bn1, seg_start, seg_count, tt1, 2,
                         None, 0, hq, hsf, I, None, 0, True, w_g=w13.global_scale, x_g=xg, out_g=g2, a_tiled=ex.tiled)
@@ -406,12 +424,17 @@ def moe_experts(h, w: torch.Tensor, ids: torch.Tensor, ex, out_dtype=torch.bfloa
     ids = ids if ids.dtype == torch.int32 else ids.int()
     _C.moe_align(ids.contiguous(), w.float().contiguous(), ex.first, E, seg_start, seg_count, row_token, row_weight,
                  pair_row, total, bn1, tt1, bn2, tt2)
-    xs = alloc_qact(max_rows, Hd, dev)
-    _C.moe_gather(a.q, a.sf, pair_row, xs.q, xs.sf)
     hq = alloc_qact(max_rows, I, dev)
     y = torch.empty(max_rows, Hd, dtype=torch.bfloat16, device=dev)
-    _expert_gemms(ex, xs.q, xs.sf, None, hq.q, hq.sf, y, Hd, bn1, bn2, seg_start, seg_count, tt1, tt2, row_weight,
-                  False)
+    if _pulls(bn1, bn2):
+        pull = dict(row_token=row_token, src_q=[a.q.data_ptr()], src_sf=[a.sf.data_ptr()], src_rows=max(T, 1))
+        _expert_gemms(ex, None, None, None, hq.q, hq.sf, y, Hd, bn1, bn2, seg_start, seg_count, tt1, tt2, row_weight,
+                      False, pull)
+    else:
+        xs = alloc_qact(max_rows, Hd, dev)
+        _C.moe_gather(a.q, a.sf, pair_row, xs.q, xs.sf)
+        _expert_gemms(ex, xs.q, xs.sf, None, hq.q, hq.sf, y, Hd, bn1, bn2, seg_start, seg_count, tt1, tt2, row_weight,
+                      False)
     if not combine:
         from . import MoEPartial
         return MoEPartial(y, pair_row, None)
@@ -463,14 +486,21 @@ def moe_experts_nvfp4(h, w, ids, ex, out_dtype=torch.bfloat16, n_experts_total=N
     ids = ids if ids.dtype == torch.int32 else ids.int()
     _C.moe_align(ids.contiguous(), w.float().contiguous(), ex.first, E, seg_start, seg_count, row_token, row_weight,
                  pair_row, total, bn1, tt1, bn2, tt2)
-    xs_q = torch.empty(max_rows, Hd // 2, dtype=torch.uint8, device=dev)
-    xs_sf = torch.empty(max_rows * (Hd // 16), dtype=torch.uint8, device=dev)
-    xs_g = torch.empty(max_rows, dtype=torch.float32, device=dev)
-    _C.moe_gather4(xq, xsf, xg, pair_row, xs_q, xs_sf, xs_g)
     hq = torch.empty(max_rows, I // 2, dtype=torch.uint8, device=dev)
     hsf = torch.empty(max_rows * (I // 16), dtype=torch.uint8, device=dev)
     y = torch.empty(max_rows, Hd, dtype=torch.bfloat16, device=dev)
-    _expert_gemms(ex, xs_q, xs_sf, xs_g, hq, hsf, y, Hd, bn1, bn2, seg_start, seg_count, tt1, tt2, row_weight, True)
+    if _pulls(bn1, bn2):
+        pull = dict(row_token=row_token, src_q=[xq.data_ptr()], src_sf=[xsf.data_ptr()], src_g=[xg.data_ptr()],
+                    src_rows=max(T, 1))
+        _expert_gemms(ex, None, None, None, hq, hsf, y, Hd, bn1, bn2, seg_start, seg_count, tt1, tt2, row_weight, True,
+                      pull)
+    else:
+        xs_q = torch.empty(max_rows, Hd // 2, dtype=torch.uint8, device=dev)
+        xs_sf = torch.empty(max_rows * (Hd // 16), dtype=torch.uint8, device=dev)
+        xs_g = torch.empty(max_rows, dtype=torch.float32, device=dev)
+        _C.moe_gather4(xq, xsf, xg, pair_row, xs_q, xs_sf, xs_g)
+        _expert_gemms(ex, xs_q, xs_sf, xs_g, hq, hsf, y, Hd, bn1, bn2, seg_start, seg_count, tt1, tt2, row_weight,
+                      True)
     if not combine:
         from . import MoEPartial
         return MoEPartial(y, pair_row, None)
@@ -481,9 +511,11 @@ def moe_experts_nvfp4(h, w, ids, ex, out_dtype=torch.bfloat16, n_experts_total=N
 
 def moe_experts_ep(h, w, ids, ex, T_step: int, n_experts_total: int, ep):
     """Expert-parallel MoE: ep_dispatch (P2P push of routed rows) -> ep_align
-    (bounded wait + routing layout over all ranks' tokens) -> ep_gather ->
-    persistent FC1 (SwiGLU + requant) -> FC2 (routing-weighted); the combine
-    + reduce-scatter runs fused in the following norm step."""
+    (bounded wait + routing layout over all ranks' tokens) -> persistent
+    FC1 (SwiGLU + requant; its producer reads the received rows in place) ->
+    FC2 (routing-weighted); the combine + reduce-scatter runs fused in the
+    following norm step.  Unfused (prefill tiles): ep_gather copies the rows
+    into an expert-sorted operand first."""
     from . import EPPartial, QAct
     from .quant import NVFP4Tensor
     fp4 = isinstance(ex.w13, NVFP4Tensor)
@@ -515,10 +547,24 @@ def moe_experts_ep(h, w, ids, ex, T_step: int, n_experts_total: int, ep):
     row_weight = torch.empty(max_rows, dtype=torch.float32, device=dev)
     pair_row = torch.empty(Tg, K, dtype=torch.int32, device=dev)
     total = torch.empty(1, dtype=torch.int32, device=dev)
+    pulls = _pulls(bn1, bn2)
     _C.ep_align(ep.bases, ep.rank, ep.max_t, Hd, K, T_step, ex.first, E, seg_start, seg_count, row_token, row_weight,
-                pair_row, total, bn1, tt1, bn2, tt2, ep.epoch, ep.err)
-    w13, w2 = ex.w13, ex.w2
+                pair_row, total, bn1, tt1, bn2, tt2, ep.epoch, ep.err, release=pulls)
     y = torch.empty(max_rows, Hd, dtype=torch.bfloat16, device=dev)
+    if pulls:
+        # received rows read in place (row index = owner rank * T_step + t);
+        # ep_align advanced the epoch, so they sit at parity (epoch + 1) & 1
+        pull = dict(row_token=row_token, src_q=[ep.recv_q], src_sf=[ep.recv_sf], src_g=[ep.recv_g] if fp4 else [],
+                    src_rows=ep.world * ep.max_t, src_epoch=ep.epoch, src_epoch_add=1, src_par_bytes=ep.par_bytes)
+        if fp4:
+            hq = torch.empty(max_rows, I // 2, dtype=torch.uint8, device=dev)
+            hsf = torch.empty(max_rows * (I // 16), dtype=torch.uint8, device=dev)
+        else:
+            h_ = alloc_qact(max_rows, I, dev)
+            hq, hsf = h_.q, h_.sf
+        _expert_gemms(ex, None, None, None, hq, hsf, y, Hd, bn1, bn2, seg_start, seg_count, tt1, tt2, row_weight, fp4,
+                      pull)
+        return EPPartial(y, pair_row, T_step, T_r)
     if fp4:
         xs_q = torch.empty(max_rows, Hd // 2, dtype=torch.uint8, device=dev)
         xs_sf = torch.empty(max_rows * (Hd // 16), dtype=torch.uint8, device=dev)

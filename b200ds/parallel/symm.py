@@ -157,6 +157,11 @@ class EPDispatch:
         self.push_ticket = torch.zeros(1, dtype=torch.int32, device=dev)
         self.gather_ticket = torch.zeros(1, dtype=torch.int32, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        # this rank's received rows, read in place by the fused expert kernel:
+        # (q, scales, global scales) addresses of parity 0 and the parity stride
+        off, self.par_bytes, off_sf, off_g = (int(v) for v in _C.ep_region_layout(self.world, max_tokens, hidden, topk))
+        mine = self.bases[self.rank] + off
+        self.recv_q, self.recv_sf, self.recv_g = mine, mine + off_sf, mine + off_g
         torch.cuda.synchronize(dev)
         dist.barrier(group=group)
 

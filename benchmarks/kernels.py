@@ -101,10 +101,11 @@ def _moe_layout(T, K, E_total, E_local, dev, bn1, bn2):
     torch.cuda.synchronize()
     active = int((seg_count > 0).sum())
     return dict(ids=ids, w=w, max_rows=max_rows, seg_start=seg_start, seg_count=seg_count, tt1=tt1, tt2=tt2,
-                row_weight=row_weight, pair_row=pair_row, active=active)
+                row_weight=row_weight, pair_row=pair_row, row_token=row_token, active=active)
 
 
-def run_moe(fmt: str, T: int, E_total: int, E_local: int, iters: int, h=7168, I=2048, tiled=False, fused=False):
+def run_moe(fmt: str, T: int, E_total: int, E_local: int, iters: int, h=7168, I=2048, tiled=False, fused=False,
+            pull=False):
     from b200ds import _C
     from b200ds.ops import cuda
     from b200ds.models.random_init import _Seeder, rand_mx, rand_nvfp4
@@ -151,16 +152,25 @@ def run_moe(fmt: str, T: int, E_total: int, E_local: int, iters: int, h=7168, I=
     if fused:
         from b200ds.ops import ExpertWeights
         ex = ExpertWeights(0, E_local, w13, w2, I, tiled=tiled, fc2_act_scale=1 / 32)
+        src = None
+        if pull:
+            # FC1 rows read in place from the T token rows (no sorted copy)
+            if fp4:
+                src = dict(row_token=L["row_token"], src_q=[xs_q.data_ptr()], src_sf=[xs_sf.data_ptr()],
+                           src_g=[xs_g.data_ptr()], src_rows=T)
+            else:
+                src = dict(row_token=L["row_token"], src_q=[xs.q.data_ptr()], src_sf=[xs.sf.data_ptr()], src_rows=T)
         if fp4:
             fn = lambda: cuda._expert_gemms(ex, xs_q, xs_sf, xs_g, hq, hsf, y, h, bn1, bn1, L["seg_start"],
-                                            L["seg_count"], L["tt1"], L["tt2"], L["row_weight"], True)
+                                            L["seg_count"], L["tt1"], L["tt2"], L["row_weight"], True, src)
         else:
             fn = lambda: cuda._expert_gemms(ex, xs.q, xs.sf, None, hqa.q, hqa.sf, y, h, bn1, bn1, L["seg_start"],
-                                            L["seg_count"], L["tt1"], L["tt2"], L["row_weight"], False)
+                                            L["seg_count"], L["tt1"], L["tt2"], L["row_weight"], False, src)
         t = timed(fn, iters)
         shape = f"{fmt} T={T} top8 E={E_local}/{E_total} active={L['active']} pairs={pairs}" + (" tiled" if tiled else "")
-        report(f"moe_fc1fc2_fused_{fmt}", shape, t, nbytes=L["active"] * wbytes, flops=2 * pairs * 3 * I * h,
-               flop_peak=peak, note=f"bn={bn1}, one launch")
+        report(f"moe_fc1fc2_fused_{fmt}" + ("_pull" if pull else ""), shape, t, nbytes=L["active"] * wbytes,
+               flops=2 * pairs * 3 * I * h, flop_peak=peak,
+               note=f"bn={bn1}, one launch" + (", rows read in place" if pull else ", pre-gathered rows"))
         return
     shape = f"{fmt} T={T} top8 E={E_local}/{E_total} active={L['active']} pairs={pairs}" + (" tiled" if tiled else "")
     t1 = timed(fc1, iters)
@@ -287,6 +297,13 @@ def main():
         ("moe_mxfp8_T64_ep8_fused", lambda: run_moe("mxfp8", 64, 256, 32, a.iters, tiled=True, fused=True)),
         ("moe_nvfp4_T256_ep8_fused", lambda: run_moe("nvfp4", 256, 256, 32, a.iters, tiled=True, fused=True)),
         ("moe_nvfp4_T64_ep1_fused", lambda: run_moe("nvfp4", 64, 256, 64 if small else 256, a.iters, fused=True)),
+        ("moe_mxfp8_T64_ep1_pull", lambda: run_moe("mxfp8", 64, 256, 64 if small else 256, a.iters, fused=True,
+                                                    pull=True)),
+        ("moe_mxfp8_T64_ep8_pull", lambda: run_moe("mxfp8", 64, 256, 32, a.iters, tiled=True, fused=True, pull=True)),
+        ("moe_nvfp4_T256_ep8_pull", lambda: run_moe("nvfp4", 256, 256, 32, a.iters, tiled=True, fused=True,
+                                                     pull=True)),
+        ("moe_nvfp4_T64_ep1_pull", lambda: run_moe("nvfp4", 64, 256, 64 if small else 256, a.iters, fused=True,
+                                                    pull=True)),
         # the same with weights stored as contiguous 128 x 128-byte tiles
         ("moe_mxfp8_T64_ep1_tiled", lambda: run_moe("mxfp8", 64, 256, 64 if small else 256, a.iters, tiled=True)),
         ("moe_mxfp8_T64_ep8_tiled", lambda: run_moe("mxfp8", 64, 256, 32, a.iters, tiled=True)),

@@ -299,7 +299,9 @@ void moe_fused(const at::Tensor& w13, const at::Tensor& w13_sf, const at::Tensor
                int64_t hidden, int64_t inter, int64_t bn, const at::Tensor& seg_start, const at::Tensor& seg_count,
                const at::Tensor& ttile_off, const at::Tensor& row_weight, at::Tensor ws, at::Tensor err,
                int64_t num_ctas, bool pdl, bool a_tiled, c10::optional<at::Tensor> x_g, c10::optional<at::Tensor> w1_g,
-               c10::optional<at::Tensor> w2_g, double out_g) {
+               c10::optional<at::Tensor> w2_g, double out_g, c10::optional<at::Tensor> row_token,
+               std::vector<int64_t> src_q, std::vector<int64_t> src_sf, std::vector<int64_t> src_g, int64_t src_rows,
+               c10::optional<at::Tensor> src_epoch, int64_t src_epoch_add, int64_t src_par_bytes) {
   check_cuda(w13, "w13");
   const c10::cuda::CUDAGuard gd(w13.device());
   TORCH_CHECK(ws.scalar_type() == at::kInt && ws.numel() >= 2 + E, "workspace int32 [2 + E]");
@@ -337,6 +339,27 @@ void moe_fused(const at::Tensor& w13, const at::Tensor& w13_sf, const at::Tensor
   a.w1_g = optr<float>(w1_g);
   a.w2_g = optr<float>(w2_g);
   a.out_g = float(out_g);
+  // pull mode: FC1 rows read from up to 8 source buffers (raw device
+  // addresses: this GPU's activations or peers' symmetric buffers)
+  a.pull = src_q.empty() ? 0 : 1;
+  if (a.pull) {
+    TORCH_CHECK(src_q.size() <= 8 && src_sf.size() == src_q.size() && row_token.has_value() && src_rows > 0,
+                "pull: <= 8 sources with scales, row_token, src_rows");
+    TORCH_CHECK(!a.fp4 || src_g.size() == src_q.size(), "pull nvfp4: per-source global scales");
+    for (size_t i = 0; i < src_q.size(); ++i) {
+      a.src_q[i] = reinterpret_cast<const uint8_t*>(src_q[i]);
+      a.src_sf[i] = reinterpret_cast<const uint8_t*>(src_sf[i]);
+      a.src_g[i] = i < src_g.size() ? reinterpret_cast<const float*>(src_g[i]) : nullptr;
+    }
+    a.src_rows = src_rows;
+    a.row_token = ptr<int>(*row_token);
+    if (src_epoch.has_value() && src_epoch->defined()) {
+      a.src_epoch = reinterpret_cast<const uint32_t*>(src_epoch->data_ptr());
+      a.src_epoch_add = int(src_epoch_add);
+      a.src_par_bytes = src_par_bytes;
+    }
+    a.rows = hq.size(0);
+  }
   check(b200_moe_fused(&a, cur_stream()), "moe_fused");
 }
 
@@ -428,7 +451,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("w_g") = pybind11::none(), pybind11::arg("x_g") = pybind11::none(),
         pybind11::arg("x_g_const") = 1.0, pybind11::arg("out_g") = 1.0, pybind11::arg("a_tiled") = false);
   m.def("nvfp4_quant", &nvfp4_quant);
-  m.def("moe_fused", &moe_fused);
+  m.def("moe_fused", &moe_fused, pybind11::arg("w13"), pybind11::arg("w13_sf"), pybind11::arg("w2"), pybind11::arg("w2_sf"),
+        pybind11::arg("x"), pybind11::arg("x_sf"), pybind11::arg("hq"), pybind11::arg("hq_sf"), pybind11::arg("y"),
+        pybind11::arg("E"), pybind11::arg("hidden"), pybind11::arg("inter"), pybind11::arg("bn"),
+        pybind11::arg("seg_start"), pybind11::arg("seg_count"), pybind11::arg("ttile_off"), pybind11::arg("row_weight"),
+        pybind11::arg("ws"), pybind11::arg("err"), pybind11::arg("num_ctas"), pybind11::arg("pdl"),
+        pybind11::arg("a_tiled"), pybind11::arg("x_g"), pybind11::arg("w1_g"), pybind11::arg("w2_g"),
+        pybind11::arg("out_g"), pybind11::arg("row_token") = pybind11::none(),
+        pybind11::arg("src_q") = std::vector<int64_t>{}, pybind11::arg("src_sf") = std::vector<int64_t>{},
+        pybind11::arg("src_g") = std::vector<int64_t>{}, pybind11::arg("src_rows") = 0,
+        pybind11::arg("src_epoch") = pybind11::none(), pybind11::arg("src_epoch_add") = 0,
+        pybind11::arg("src_par_bytes") = 0);
   m.def("moe_gather4", &moe_gather4);
   m.def("num_sms", &num_sms);
   m.def("graph_kernel_count", &graph_kernel_count);

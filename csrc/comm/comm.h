@@ -81,10 +81,12 @@ int b200_ep_dispatch(const uint8_t* q, const uint8_t* sf, const float* g, int fp
                      int T_r, int T_step, int experts_per_rank, const EpPeers* peers, const uint32_t* epoch,
                      uint32_t* ticket, cudaStream_t st);
 // Routing layout over the received world * T_step tokens (waits for every
-// rank's dispatch; bounded).
+// rank's dispatch; bounded).  release = 1 (no ep_gather follows: the expert
+// GEMM reads the received rows in place): also frees the parity (counters to
+// zero, epoch + 1), so the consumer finds the rows at parity (epoch + 1) & 1.
 int b200_ep_align(const EpPeers* peers, int T_step, int first, int E, int* seg_start, int* seg_count, int* row_token,
                   float* row_weight, int* pair_row, int* total_rows, int bn1, int* ttile1, int bn2, int* ttile2,
-                  const uint32_t* epoch, uint32_t* err, cudaStream_t st);
+                  uint32_t* epoch, uint32_t* err, int release, cudaStream_t st);
 // Gather received rows into the expert-sorted operand; the last CTA frees
 // the parity (counters to zero, epoch + 1).
 int b200_ep_gather(const EpPeers* peers, int T_step, const int* pair_row, int fp4, uint8_t* dq, uint8_t* dsf, float* dg,

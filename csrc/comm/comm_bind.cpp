@@ -83,6 +83,14 @@ EpPeers make_ep(const std::vector<int64_t>& bases, int64_t rank, int64_t max_t, 
   return p;
 }
 
+// (region offset, parity bytes, scale offset, global-scale offset) of the
+// dispatch buffer: the fused expert GEMM reads received rows in place.
+std::vector<int64_t> ep_region_layout(int64_t world, int64_t max_t, int64_t hidden, int64_t K) {
+  int64_t pb, off_sf, off_ids, off_w, off_g;
+  ep_layout(world, max_t, hidden, K, &pb, &off_sf, &off_ids, &off_w, &off_g);
+  return {kEpRegionOff, pb, off_sf, off_g};
+}
+
 int64_t ep_buffer_size(int64_t world, int64_t max_t, int64_t hidden, int64_t K) {
   return ep_buffer_bytes(world, max_t, hidden, K);
 }
@@ -111,15 +119,15 @@ void ep_dispatch(const at::Tensor& q, const at::Tensor& sf, c10::optional<at::Te
 void ep_align(std::vector<int64_t> bases, int64_t rank, int64_t max_t, int64_t hidden, int64_t K, int64_t T_step,
               int64_t first, int64_t E, at::Tensor seg_start, at::Tensor seg_count, at::Tensor row_token,
               at::Tensor row_weight, at::Tensor pair_row, at::Tensor total_rows, int64_t bn1, at::Tensor ttile1,
-              int64_t bn2, at::Tensor ttile2, const at::Tensor& epoch, at::Tensor err) {
+              int64_t bn2, at::Tensor ttile2, const at::Tensor& epoch, at::Tensor err, bool release) {
   const c10::cuda::CUDAGuard g(pair_row.device());
   EpPeers p = make_ep(bases, rank, max_t, hidden, K);
   TORCH_CHECK(pair_row.numel() == p.world * T_step * K, "pair_row [world*T_step, K]");
   const int rc = b200_ep_align(&p, T_step, first, E, seg_start.data_ptr<int>(), seg_count.data_ptr<int>(),
                                row_token.data_ptr<int>(), row_weight.data_ptr<float>(), pair_row.data_ptr<int>(),
                                total_rows.data_ptr<int>(), bn1, ttile1.data_ptr<int>(), bn2, ttile2.data_ptr<int>(),
-                               reinterpret_cast<const uint32_t*>(epoch.data_ptr()),
-                               reinterpret_cast<uint32_t*>(err.data_ptr()), cur());
+                               reinterpret_cast<uint32_t*>(epoch.data_ptr()),
+                               reinterpret_cast<uint32_t*>(err.data_ptr()), release ? 1 : 0, cur());
   TORCH_CHECK(rc == 0, "ep_align failed ", rc);
 }
 
@@ -203,8 +211,14 @@ void register_comm(pybind11::module& m) {
   m.def("ar_buffer_size", &ar_buffer_size);
   m.def("moe_combine_push", &moe_combine_push);
   m.def("ep_buffer_size", &ep_buffer_size);
+  m.def("ep_region_layout", &ep_region_layout);
   m.def("ep_dispatch", &ep_dispatch);
-  m.def("ep_align", &ep_align);
+  m.def("ep_align", &ep_align, pybind11::arg("bases"), pybind11::arg("rank"), pybind11::arg("max_t"),
+        pybind11::arg("hidden"), pybind11::arg("K"), pybind11::arg("T_step"), pybind11::arg("first"), pybind11::arg("E"),
+        pybind11::arg("seg_start"), pybind11::arg("seg_count"), pybind11::arg("row_token"), pybind11::arg("row_weight"),
+        pybind11::arg("pair_row"), pybind11::arg("total_rows"), pybind11::arg("bn1"), pybind11::arg("ttile1"),
+        pybind11::arg("bn2"), pybind11::arg("ttile2"), pybind11::arg("epoch"), pybind11::arg("err"),
+        pybind11::arg("release") = false);
   m.def("ep_gather", &ep_gather);
   m.def("ep_combine_rs", &ep_combine_rs);
   m.def("lm_candidates", &lm_candidates);

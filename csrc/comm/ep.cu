@@ -13,7 +13,11 @@
 //                 builds the grouped-GEMM routing layout over all received
 //                 rows (experts outside this rank's range are skipped).
 //   ep_gather     copies the received rows into the expert-sorted operand of
-//                 the grouped FC1 GEMM; its last CTA frees the parity.
+//                 the grouped FC1 GEMM; its last CTA frees the parity.  With
+//                 the fused expert kernel this step disappears: its producer
+//                 warp reads each sorted row straight from the dispatch
+//                 buffer (cp.async, 128B-swizzled into the operand tile) and
+//                 ep_align frees the parity instead (release = 1).
 //   ep_combine_rs after FC2 (whose epilogue already applied the routing
 //                 weights): sums each received token's rows over this rank's
 //                 experts and stores the partial straight into the owner
@@ -21,7 +25,7 @@
 //                 ar_reduce_norm sums the world partials in rank order, adds
 //                 the residual, RMSNorm and MXFP8 - one fused kernel.
 //
-// Two parities alternate (device epoch advanced by ep_gather), as in the
+// Two parities alternate (device epoch advanced by ep_gather or ep_align), as in the
 // tensor-parallel all-reduce: a rank pushes into parity p again only after
 // its reduce-scatter of the previous layer, which waited for every peer's
 // combine, which each peer issued after its gather had released p.
@@ -96,7 +100,7 @@ __global__ void __launch_bounds__(kThreads) ep_dispatch_kernel(const uint8_t* __
 __global__ void __launch_bounds__(1024) ep_align_kernel(EpPeers P, int T_step, int first, int E, int* seg_start,
                                                         int* seg_count, int* row_token, float* row_weight,
                                                         int* pair_row, int* total_rows, int bn1, int* ttile1, int bn2,
-                                                        int* ttile2, const uint32_t* epoch, uint32_t* err) {
+                                                        int* ttile2, uint32_t* epoch, uint32_t* err, int release) {
   extern __shared__ int sh[];
   __shared__ int ok_s;
   pdl_wait();
@@ -113,6 +117,18 @@ __global__ void __launch_bounds__(1024) ep_align_kernel(EpPeers P, int T_step, i
   moe::moe_align_body(reinterpret_cast<const int*>(reg + P.off_ids), reinterpret_cast<const float*>(reg + P.off_w), T,
                       P.K, first, E, seg_start, seg_count, row_token, row_weight, pair_row, total_rows, bn1, ttile1, bn2,
                       ttile2, sh);
+  if (release) {
+    // every thread read the epoch above; the rows stay in place for the
+    // expert GEMM of this layer, and the next push into parity p comes two
+    // layers on, after this rank's reduce-scatter of the next layer
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t* cnt = comm::counters(mine, p);
+      for (int s = 0; s < P.world; ++s) atomicExch(cnt + s, 0u);
+      __threadfence();
+      atomicAdd(epoch, 1u);
+    }
+  }
 }
 
 __global__ void __launch_bounds__(kThreads) ep_gather_kernel(EpPeers P, int T_step, const int* pair_row, int fp4,
@@ -220,11 +236,11 @@ int b200_ep_dispatch(const uint8_t* q, const uint8_t* sf, const float* g, int fp
 
 int b200_ep_align(const EpPeers* peers, int T_step, int first, int E, int* seg_start, int* seg_count, int* row_token,
                   float* row_weight, int* pair_row, int* total_rows, int bn1, int* ttile1, int bn2, int* ttile2,
-                  const uint32_t* epoch, uint32_t* err, cudaStream_t st) {
+                  uint32_t* epoch, uint32_t* err, int release, cudaStream_t st) {
   if (T_step <= 0 || T_step > peers->max_t) return -1;
   b200::launch_pdl(b200::ep::ep_align_kernel, dim3(1), dim3(1024), 3 * E * sizeof(int), st, *peers, T_step, first, E,
                    seg_start, seg_count, row_token, row_weight, pair_row, total_rows, bn1 > 0 ? bn1 : 128, ttile1,
-                   bn2 > 0 ? bn2 : 128, ttile2, epoch, err);
+                   bn2 > 0 ? bn2 : 128, ttile2, epoch, err, release);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
 

@@ -121,6 +121,21 @@ struct MoeFusedArgs {
   const float* w1_g;       // NVFP4: per expert
   const float* w2_g;
   float out_g;             // NVFP4: global scale of the FC1 output
+  // pull = 1: the FC1 activation rows are read straight from their source
+  // buffers (this GPU's or a peer's, P2P) by the producer warp instead of a
+  // pre-gathered x: sorted row r is token row_token[r] = s * src_rows + t,
+  // i.e. row t of source s (q rows, scales in the tcgen05 layout, NVFP4 g).
+  int pull;
+  const uint8_t* src_q[8];
+  const uint8_t* src_sf[8];
+  const float* src_g[8];
+  int src_rows;
+  const int* row_token;
+  // sources in a two-parity buffer: every source pointer moves by
+  // ((*src_epoch + src_epoch_add) & 1) * src_par_bytes (null: fixed sources)
+  const uint32_t* src_epoch;
+  int src_epoch_add;
+  int64_t src_par_bytes;
 };
 int b200_moe_fused(const MoeFusedArgs* args, cudaStream_t stream);
 

@@ -76,6 +76,18 @@ struct Params {
   int* fc1_done;             // [E] finished FC1 units per expert
   uint32_t* err;
   int a_tiled;
+  // pull mode: FC1 activation rows straight from their source buffers
+  int pull;
+  const uint8_t* src_q[8];
+  const uint8_t* src_sf[8];
+  const float* src_g[8];
+  int src_rows;
+  const int* row_token;
+  // sources in a two-parity buffer: every source pointer moves by
+  // ((*src_epoch + src_epoch_add) & 1) * src_par_bytes (null: fixed sources)
+  const uint32_t* src_epoch;
+  int src_epoch_add;
+  int64_t src_par_bytes;
 };
 
 __device__ __forceinline__ int64_t sf_offset(int row, int kblock, int kb_total) {
@@ -143,11 +155,17 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap tm_w1, const __grid_constan
   int* tile_q = reinterpret_cast<int*>(tq_empty + kRing);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tile_q + kRing);
   __shared__ int lay[3 * kMaxExperts + 1];
+  // pull mode: the current FC1 unit's row sources, resolved once per unit
+  // (row address, scale base, row index in its source; null = padding row)
+  __shared__ const uint8_t* pull_q[BN];
+  __shared__ const uint8_t* pull_sf[BN];
+  __shared__ int pull_row[BN];
 
   const int warp = warp_id(), lane = lane_id();
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(&full[s], 1);
+      // pull mode: lane 0's expect-tx arrival + one per producer lane after its copies
+      mbar_init(&full[s], p.pull ? 33 : 1);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -197,36 +215,48 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap tm_w1, const __grid_constan
 
   if (warp == 0) {
     // ------------------------------ producer ------------------------------
-    if (lane == 0) {
-      const uint64_t pol_w = policy_evict_first();
-      const uint64_t pol_x = policy_evict_last();
-      int it = 0;
-      for (int q = 0;; ++q) {
-        const int slot = q % kRing;
-        if (q >= kRing && !mbar_wait(&tq_empty[slot], ((q / kRing) - 1) & 1, p.err)) break;
-        int u = atomicAdd(p.work, 1);
+    // Lane 0 grabs units and issues the TMA loads of the weights (and, unless
+    // pulling, of the activations); in pull mode every lane also gathers the
+    // FC1 activation rows of the stage with 16-byte cp.async (P2P for peer
+    // rows) into the 128B-swizzled tile, plus their scale words.
+    const uint64_t pol_w = policy_evict_first();
+    const uint64_t pol_x = policy_evict_last();
+    const int kbq1 = FP4 ? p.hidden / 16 : p.hidden / 32;     // activation scale columns
+  const int64_t par_off =
+      p.src_epoch ? (int64_t)((__ldcg(p.src_epoch) + (uint32_t)p.src_epoch_add) & 1u) * p.src_par_bytes : 0;
+    int it = 0;
+    for (int q = 0;; ++q) {
+      const int slot = q % kRing;
+      if (q >= kRing && !__all_sync(0xffffffffu, mbar_wait(&tq_empty[slot], ((q / kRing) - 1) & 1, p.err))) break;
+      int u = 0;
+      if (lane == 0) {
+        u = atomicAdd(p.work, 1);
         if (u >= U) u = -1;
         tile_q[slot] = u;
         mbar_arrive(&tq_full[slot]);
-        if (u < 0) break;
-        const Unit d = decode(u, U1, n1, n2, lay, E);
-        const int b_row = lay[E + 1 + d.e] + d.tt * BN;
-        int nk, a_row0, a_row1, kct;
-        const CUtensorMap *ma, *mb;
-        const uint8_t *sfa, *sfb;
-        if (d.fc1) {
-          nk = kb1 / kTileK;
-          a_row0 = d.e * 2 * p.inter + d.n * kTileM;
-          a_row1 = a_row0 + p.inter;
-          ma = &tm_w1;
-          mb = &tm_x;
-          sfa = p.sfa1 + (int64_t)d.e * p.sfa1_estride;
-          sfb = p.sfb1;
-          kct = kct1;
-        } else {
-          // the expert's FC1 output must be complete (bounded wait)
-          // (skipped once any wait of this launch has given up, so a failed
-          // launch ends after one deadline instead of one per unit)
+      }
+      u = __shfl_sync(0xffffffffu, u, 0);
+      if (u < 0) break;
+      const Unit d = decode(u, U1, n1, n2, lay, E);
+      const int b_row = lay[E + 1 + d.e] + d.tt * BN;
+      const bool pulled = p.pull && d.fc1;
+      int nk, a_row0, a_row1, kct;
+      const CUtensorMap *ma, *mb;
+      const uint8_t *sfa, *sfb;
+      if (d.fc1) {
+        nk = kb1 / kTileK;
+        a_row0 = d.e * 2 * p.inter + d.n * kTileM;
+        a_row1 = a_row0 + p.inter;
+        ma = &tm_w1;
+        mb = &tm_x;
+        sfa = p.sfa1 + (int64_t)d.e * p.sfa1_estride;
+        sfb = p.sfb1;
+        kct = kct1;
+      } else {
+        if (lane == 0) {
+          // the expert's FC1 output must be complete (bounded wait; skipped
+          // once any wait of this launch has given up, so a failed launch
+          // ends after one deadline instead of one per unit)
           const int need = n1 * (lay[d.e + 1] - lay[d.e]);
           const uint64_t t0 = globaltimer_ns();
           while (ld_acquire_gpu(p.fc1_done + d.e) < need && *reinterpret_cast<volatile uint32_t*>(p.err) == 0) {
@@ -236,22 +266,50 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap tm_w1, const __grid_constan
             }
           }
           fence_proxy_async_global();
-          nk = kb2 / kTileK;
-          a_row0 = d.e * p.hidden + d.n * 2 * kTileM;
-          a_row1 = a_row0 + kTileM;
-          ma = &tm_w2;
-          mb = &tm_h;
-          sfa = p.sfa2 + (int64_t)d.e * p.sfa2_estride;
-          sfb = p.hq_sf;
-          kct = kct2;
         }
-        const int rb0 = (a_row0 - d.e * (d.fc1 ? 2 * p.inter : p.hidden)) >> 7;
-        const int rb1 = (a_row1 - d.e * (d.fc1 ? 2 * p.inter : p.hidden)) >> 7;
-        bool ok = true;
-        for (int kt = 0; kt < nk; ++kt, ++it) {
-          const int s = it % C::kStages;
-          if (it >= C::kStages && !mbar_wait(&empty[s], ((it / C::kStages) - 1) & 1, p.err)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[s], C::kLoadBytes);
+        __syncwarp();
+        nk = kb2 / kTileK;
+        a_row0 = d.e * p.hidden + d.n * 2 * kTileM;
+        a_row1 = a_row0 + kTileM;
+        ma = &tm_w2;
+        mb = &tm_h;
+        sfa = p.sfa2 + (int64_t)d.e * p.sfa2_estride;
+        sfb = p.hq_sf;
+        kct = kct2;
+      }
+      const int rb0 = (a_row0 - d.e * (d.fc1 ? 2 * p.inter : p.hidden)) >> 7;
+      const int rb1 = (a_row1 - d.e * (d.fc1 ? 2 * p.inter : p.hidden)) >> 7;
+      const int tmax = d.rows - d.tt * BN;
+      if (pulled) {
+        __syncwarp();
+        for (int j = lane; j < BN; j += 32) {
+          const uint8_t *rq = nullptr, *rs = nullptr;
+          int lr = 0;
+          if (j < tmax) {
+            const int g = __ldcg(p.row_token + b_row + j);
+            const int sr = g / p.src_rows;
+            lr = g - sr * p.src_rows;
+            rq = p.src_q[sr] + par_off + (int64_t)lr * kb1;
+            rs = p.src_sf[sr] + par_off;
+          }
+          pull_q[j] = rq;
+          pull_sf[j] = rs;
+          pull_row[j] = lr;
+        }
+        __syncwarp();
+      }
+      bool ok = true;
+      for (int kt = 0; kt < nk; ++kt, ++it) {
+        const int s = it % C::kStages;
+        if (it >= C::kStages &&
+            !__all_sync(0xffffffffu, mbar_wait(&empty[s], ((it / C::kStages) - 1) & 1, p.err))) {
+          ok = false;
+          break;
+        }
+        uint8_t* sfb_dst = sSFB + (size_t)s * 2 * C::kSfK;
+        const int kc0 = kt * kChunksPerTile;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[s], pulled ? C::kLoadBytes - BN * kTileK - C::kSfK : C::kLoadBytes);
           uint8_t* a_dst = sA + (size_t)s * 2 * kTileM * kTileK;
           if (p.a_tiled) {
             tma_load_3d_hint(a_dst, ma, &full[s], 0, 0, (a_row0 >> 7) * nk + kt, pol_w);
@@ -260,17 +318,42 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap tm_w1, const __grid_constan
             tma_load_2d_hint(a_dst, ma, &full[s], kt * kTileK, a_row0, pol_w);
             tma_load_2d_hint(a_dst + kTileM * kTileK, ma, &full[s], kt * kTileK, a_row1, pol_w);
           }
-          tma_load_2d_hint(sB + (size_t)s * BN * kTileK, mb, &full[s], kt * kTileK, b_row, pol_x);
           uint8_t* sfa_dst = sSFA + (size_t)s * 2 * C::kSfK;
-          const int kc0 = kt * kChunksPerTile;
           bulk_load_hint(sfa_dst, sfa + ((int64_t)(rb0 * kct + kc0) << 9), C::kSfK, &full[s], pol_w);
           bulk_load_hint(sfa_dst + C::kSfK, sfa + ((int64_t)(rb1 * kct + kc0) << 9), C::kSfK, &full[s], pol_w);
-          bulk_load_hint(sSFB + (size_t)s * 2 * C::kSfK, sfb + ((int64_t)((b_row >> 7) * kct + kc0) << 9), C::kSfK,
-                         &full[s], pol_x);
+          if (!pulled) {
+            tma_load_2d_hint(sB + (size_t)s * BN * kTileK, mb, &full[s], kt * kTileK, b_row, pol_x);
+            bulk_load_hint(sfb_dst, sfb + ((int64_t)((b_row >> 7) * kct + kc0) << 9), C::kSfK, &full[s], pol_x);
+          }
         }
-        if (!ok) break;
+        if (p.pull) {
+          if (pulled) {
+            const uint32_t bdst = smem_u32(sB + (size_t)s * BN * kTileK);
+#pragma unroll
+            for (int i = 0; i < BN / 4; ++i) {
+              const int j = (lane >> 3) + 4 * i, c = lane & 7;
+              const uint8_t* rq = pull_q[j];
+              cp_async_16(bdst + j * kTileK + ((c ^ (j & 7)) << 4), rq ? rq + kt * kTileK + c * 16 : p.src_q[0],
+                          rq ? 16u : 0u);
+            }
+            const uint32_t sdst = smem_u32(sfb_dst);
+            for (int idx = lane; idx < BN * kChunksPerTile; idx += 32) {
+              const int j = idx / kChunksPerTile, ch = idx - j * kChunksPerTile;
+              const uint8_t* rs = pull_sf[j];
+              cp_async_4(sdst + ch * kSf + (j & 31) * 16 + (j >> 5) * 4,
+                         rs ? rs + sf_offset(pull_row[j], 4 * (kc0 + ch), kbq1) : p.src_sf[0], rs ? 4u : 0u);
+            }
+            // each lane's arrival fires when its copies have landed; the MMA
+            // thread fences them into the async proxy after its wait
+            cp_async_mbar_arrive_noinc(&full[s]);
+          } else {
+            mbar_arrive(&full[s]);
+          }
+        }
       }
+      if (!ok) break;
     }
+    if (p.pull) cp_async_wait_all();   // nothing lands after this warp has left (error exits)
   } else if (warp == 1) {
     // ------------------------------ MMA issuer ----------------------------
     int it = 0;
@@ -293,7 +376,8 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap tm_w1, const __grid_constan
         const int s = it % C::kStages;
         if (!mbar_wait(&full[s], (it / C::kStages) & 1, p.err)) { ok = false; break; }
         tc_fence_after();
-        const int o = b_row & 127;
+        if (p.pull && d.fc1) fence_proxy_async_smem();   // cp.async (generic proxy) rows -> tcgen05 reads
+        const int o = (p.pull && d.fc1) ? 0 : (b_row & 127);   // pulled rows sit at tile-local positions
         uint8_t* sfb_stage = sSFB + (size_t)s * 2 * C::kSfK;
         if (o != 0) {
           for (int ch = 0; ch < kChunksPerTile; ++ch)
@@ -346,6 +430,8 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap tm_w1, const __grid_constan
     const int sub = warp & 3;
     const int tid = threadIdx.x - 64;
     const int kbq = FP4 ? p.inter / 16 : p.inter / 32;   // scale columns of h
+    const int64_t g_off =
+        p.src_epoch ? (int64_t)((__ldcg(p.src_epoch) + (uint32_t)p.src_epoch_add) & 1u) * p.src_par_bytes : 0;
     for (int q = 0;; ++q) {
       const int slot = q % kRing;
       if (!mbar_wait(&tq_full[slot], (q / kRing) & 1, p.err)) break;
@@ -373,7 +459,19 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap tm_w1, const __grid_constan
           for (int j = 0; j < 16; ++j) {
             const int orow = b_row + c0 + j;
             if constexpr (FP4) {
-              const float sc = wg * __ldcg(p.x_g + orow);
+              float xg = 0.f;
+              if (p.pull) {
+                // padding rows of the segment have no token (row_token unset)
+                if (c0 + j < tmax) {
+                  const int gi = __ldcg(p.row_token + orow);
+                  const int sr = gi / p.src_rows;
+                  xg = __ldcg(reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(p.src_g[sr]) + g_off) +
+                              (gi - sr * p.src_rows));
+                }
+              } else {
+                xg = __ldcg(p.x_g + orow);
+              }
+              const float sc = wg * xg;
               const float gv = __uint_as_float(g[j]) * sc;
               const float h = gv / (1.0f + __expf(-gv)) * (__uint_as_float(uu[j]) * sc);
               float amax = fabsf(h);
@@ -506,7 +604,7 @@ static int launch(const MoeFusedArgs& a, cudaStream_t st) {
   const int64_t r1 = (int64_t)a.E * 2 * a.inter, r2 = (int64_t)a.E * a.hidden;
   if (a.a_tiled ? map_tiled(&m1, a.w13, r1, kb1) : map2d(&m1, a.w13, r1, kb1, kTileM)) return -2;
   if (a.a_tiled ? map_tiled(&m2, a.w2, r2, kb2) : map2d(&m2, a.w2, r2, kb2, kTileM)) return -2;
-  if (map2d(&mx, a.x, a.rows, kb1, BN)) return -3;
+  if (map2d(&mx, a.pull ? a.hq : a.x, a.rows, a.pull ? kb2 : kb1, BN)) return -3;   // unused when pulling
   if (map2d(&mh, a.hq, a.rows, kb2, BN)) return -3;
   Params p{};
   p.sfa1 = a.w13_sf;
@@ -533,6 +631,17 @@ static int launch(const MoeFusedArgs& a, cudaStream_t st) {
   p.fc1_done = a.fc1_done;
   p.err = a.err;
   p.a_tiled = a.a_tiled;
+  p.pull = a.pull;
+  for (int i = 0; i < 8; ++i) {
+    p.src_q[i] = a.src_q[i];
+    p.src_sf[i] = a.src_sf[i];
+    p.src_g[i] = a.src_g[i];
+  }
+  p.src_rows = a.src_rows;
+  p.row_token = a.row_token;
+  p.src_epoch = a.src_epoch;
+  p.src_epoch_add = a.src_epoch_add;
+  p.src_par_bytes = a.src_par_bytes;
   auto kern = moe_fused_kernel<BN, FP4>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
   cudaLaunchConfig_t cfg = {};
@@ -566,8 +675,11 @@ int b200_moe_fused(const MoeFusedArgs* a, cudaStream_t st) {
   if (a->E > kMaxExperts || a->E <= 0 || a->num_ctas <= 0 || a->hidden % 256 || a->inter % 128 || !a->work ||
       !a->fc1_done)
     return -1;
+  if (a->pull && (a->src_rows <= 0 || !a->row_token || !a->src_q[0] || !a->src_sf[0])) return -1;
   if (a->fp4) {
-    if (a->hidden % 256 || a->inter % 256 || !a->w1_g || !a->w2_g || !a->x_g || a->out_g <= 0.f) return -1;
+    if (a->hidden % 256 || a->inter % 256 || !a->w1_g || !a->w2_g || (!a->x_g && !a->pull) ||
+        (a->pull && !a->src_g[0]) || a->out_g <= 0.f)
+      return -1;
     return launch_bn<true>(*a, st);
   }
   return launch_bn<false>(*a, st);

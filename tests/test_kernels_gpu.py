@@ -556,7 +556,8 @@ def test_sample_tokens_matches_reference(V):
 def test_moe_fused_matches_two_launch(fp4, tiled, T, skew):
     """The fused persistent FC1+FC2 kernel (dynamic work grabbing, per-expert
     FC1 -> FC2 dependencies) gives bit-identical outputs to the two grouped
-    launches, also when every token goes to a few experts."""
+    launches, with the FC1 rows gathered first or read in place by its
+    producer warp, also when every token goes to a few experts."""
     from b200ds.ops import ExpertWeights, cuda
     from b200ds.ops.quant import MXFP8Tensor, NVFP4Tensor, tile_rows128
     torch.manual_seed(7)
@@ -579,18 +580,20 @@ def test_moe_fused_matches_two_launch(fp4, tiled, T, skew):
     wts = torch.rand(T, K, device=DEV)
     run = (lambda: cuda.moe_experts_nvfp4(x, wts, ids, ex, torch.float32)) if fp4 else \
         (lambda: cuda.moe_experts(cuda.quant(x), wts, ids, ex, torch.float32))
-    old = cuda.MOE_FUSED
+    old = cuda.MOE_FUSED, cuda.MOE_PULL
     try:
         cuda.MOE_FUSED = False
         a = run()
-        cuda.MOE_FUSED = True
-        b = run()
+        cuda.MOE_FUSED, cuda.MOE_PULL = True, False
+        d = run()                  # fused, rows gathered into a sorted copy first
+        cuda.MOE_PULL = True
+        b = run()                  # fused, producer reads the rows in place
         c = run()                  # counters reset by the previous launch
     finally:
-        cuda.MOE_FUSED = old
+        cuda.MOE_FUSED, cuda.MOE_PULL = old
     torch.cuda.synchronize()
     cuda.check_device_errors()
-    assert torch.equal(a, b) and torch.equal(b, c)
+    assert torch.equal(a, d) and torch.equal(a, b) and torch.equal(b, c)
 
 
 def test_mla_fused_rope_query_prep():
