@@ -148,8 +148,10 @@ def _dp_rank(rank, world, comm_impl, fmt="mxfp8"):
 def test_dp2_ep2_matches_single_gpu(comm_impl, fmt):
     """DP attention + EP MoE on 2 GPUs, ranks with different token counts:
     each rank's logits follow a 1-GPU run of its own batch (fp8 noise only).
-    The fused path exercises ep_dispatch / ep_align / ep_gather and the
-    combine + reduce-scatter into ar_reduce_norm."""
+    The fused path exercises ep_dispatch / ep_align, the expert kernel
+    reading the received rows in place from the dispatch buffer (alternating
+    parities over the layers) and the combine + reduce-scatter into
+    ar_reduce_norm."""
     _needs(2)
     res = run_ranks(_dp_rank, 2, comm_impl, fmt, timeout=600)
     for rank, out, ref in res:
