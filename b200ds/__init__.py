@@ -21,14 +21,25 @@ __all__ = ["Engine", "EngineConfig", "ModelConfig", "SamplingParams", "GenerateO
 
 def build_model_from(cfg: ModelConfig, ecfg: EngineConfig, weights: Union[str, dict] = "random",
                      device=None, seed: int = 0, ps=None):
-    """Build this rank's DeepseekModel.  ``weights`` is "random" (random init
-    of the architecture), a checkpoint directory, or a full state dict."""
+    """Build this rank's model (DeepseekModel, or DeepseekV4Model for
+    arch="deepseek_v4").  ``weights`` is "random" (random init of the
+    architecture), a checkpoint directory, or a full state dict."""
     from .parallel.state import get_state
     from .models import loader
     from .models.reference import init_weights
     ps = ps or get_state()
     if device is None:
         device = ps.device if ps.device.type == "cuda" else ("cuda" if torch.cuda.is_available() else "cpu")
+    if cfg.is_v4:
+        from .models.deepseek_v4 import build_model_v4
+        from .models.reference_v4 import init_weights_v4
+        if isinstance(weights, dict):
+            sd = weights
+        elif weights == "random":
+            sd = init_weights_v4(cfg, seed=seed)
+        else:
+            sd = loader.load_checkpoint(weights)
+        return build_model_v4(cfg, ecfg, ps, sd, device=device)
     if isinstance(weights, dict):
         sd = weights
     elif weights == "random":

@@ -56,10 +56,47 @@ class ModelConfig:
     # (e2m1 + e4m3 per 16 along K + fp32 global), "bf16" or "fp32".
     dense_format: str = "mxfp8"
     expert_format: str = "mxfp8"
+    # ---- DeepSeek-V4-family architecture (arch="deepseek_v4"; all off for V3) ----
+    # mHC: hc_mult residual streams mixed per sublayer by coefficients computed
+    # from the streams (pre: combine into the sublayer input, post: spread the
+    # output, comb: Sinkhorn-normalised stream mixing).
+    arch: str = "deepseek_v3"
+    hc_mult: int = 0
+    hc_sinkhorn_iters: int = 20
+    hc_eps: float = 1e-6
+    # MQA latent attention: one shared K=V row of kv_lora_rank per token whose
+    # last qk_rope_head_dim dims carry RoPE; queries of kv_lora_rank per head;
+    # per-head softmax sinks; the output's rope tail is rotated back; output
+    # projection = grouped low-rank wo_a (o_groups x o_lora_rank) then wo_b.
+    o_lora_rank: int = 0
+    o_groups: int = 0
+    attn_sink: bool = False
+    # E5 routed-expert prune at decode (budget 0 = off): an expert picked by at
+    # most prune_max_count rows is dropped when each picker's cumulative mass up
+    # to it (lightest first) stays within prune_budget of the row's mass.
+    prune_budget: float = 0.0
+    prune_max_count: int = 1
+    # Engram: hashed n-gram lookups into host-memory e4m3 tables (rows of
+    # engram_dim bytes + UE8M0 per 32) before these layers, gated into every
+    # residual stream.
+    engram_layers: tuple = ()
+    engram_heads: int = 0
+    engram_dim: int = 256
+    engram_rows: int = 0
+    engram_max_ngram: int = 3
+    engram_clamp: float = 10.0
+    # layers whose residual-stream mean is exported (draft-model taps)
+    aux_layers: tuple = ()
 
     # ---- derived -----------------------------------------------------------
     @property
+    def is_v4(self) -> bool:
+        return self.arch == "deepseek_v4"
+
+    @property
     def qk_head_dim(self) -> int:
+        if self.is_v4:
+            return self.kv_lora_rank
         return self.qk_nope_head_dim + self.qk_rope_head_dim
 
     @property
@@ -73,6 +110,8 @@ class ModelConfig:
     @property
     def softmax_scale(self) -> float:
         s = 1.0 / math.sqrt(self.qk_head_dim)
+        if self.is_v4:
+            return s
         rs = self.rope_scaling
         if rs and rs.get("type", rs.get("rope_type")) == "yarn":
             m = yarn_mscale(rs["factor"], rs.get("mscale_all_dim", 0.0))
@@ -83,6 +122,19 @@ class ModelConfig:
         h = self.hidden_size
         H = self.num_attention_heads
         qr = self.q_lora_rank or 0
+        if self.is_v4:
+            L = self.kv_lora_rank
+            attn = h * (qr + L) + qr * H * L + self.o_groups * self.o_lora_rank * (H // self.o_groups) * L
+            attn += h * self.o_groups * self.o_lora_rank
+            moe = (self.n_routed_experts + self.n_shared_experts) * 3 * h * self.moe_intermediate_size
+            moe += self.n_routed_experts * h
+            n_moe = sum(1 for i in range(self.num_hidden_layers) if self.is_moe_layer(i))
+            dense = 3 * h * self.intermediate_size
+            hc = 2 * (2 + self.hc_mult) * self.hc_mult * self.hc_mult * h if self.hc_mult else 0
+            emb = self.vocab_size * h * (1 if self.tie_word_embeddings else 2)
+            eng = len(self.engram_layers) * 2 * h * self.engram_heads * self.engram_dim
+            return (self.num_hidden_layers * (attn + hc) + n_moe * moe + (self.num_hidden_layers - n_moe) * dense
+                    + emb + eng)
         attn = (h * qr + qr * H * self.qk_head_dim if qr else h * H * self.qk_head_dim)
         attn += h * self.kv_cache_dim + self.kv_lora_rank * H * (self.qk_nope_head_dim + self.v_head_dim)
         attn += H * self.v_head_dim * h
@@ -168,12 +220,67 @@ def small_gpu_config(**over) -> ModelConfig:
     return dataclasses.replace(c, **over)
 
 
+def tiny_v4_config(**over) -> ModelConfig:
+    """DeepSeek-V4-family CPU/gloo test model: 3 layers (dense, MoE, MoE),
+    hidden 256, 4 MQA heads of 64 (rope tail 16), 2 output groups of rank 64,
+    4 mHC streams, 8 experts top-2 with sqrt-softplus scoring and the E5
+    prune, one Engram layer (4 hash heads)."""
+    c = ModelConfig(
+        arch="deepseek_v4", vocab_size=1024, hidden_size=256, intermediate_size=512, moe_intermediate_size=128,
+        num_hidden_layers=3, first_k_dense_replace=1, num_attention_heads=4, q_lora_rank=128, kv_lora_rank=64,
+        qk_nope_head_dim=48, qk_rope_head_dim=16, v_head_dim=64, o_lora_rank=64, o_groups=2, attn_sink=True,
+        n_routed_experts=8, n_shared_experts=1, num_experts_per_tok=2, n_group=1, topk_group=1,
+        routed_scaling_factor=1.5, scoring_func="sqrtsoftplus", prune_budget=0.4, prune_max_count=1,
+        hc_mult=4, hc_sinkhorn_iters=8, engram_layers=(1,), engram_heads=4, engram_dim=256, engram_rows=512,
+        aux_layers=(2,), max_position_embeddings=4096, rope_scaling=None, dense_format="fp32",
+        expert_format="fp32")
+    return dataclasses.replace(c, **over)
+
+
+def small_v4_gpu_config(**over) -> ModelConfig:
+    """A V4-family model for single-GPU tests on the tensor-core paths: 16
+    heads of 512 (rope 64) in 4 output groups of rank 512, 32 experts top-6,
+    4 mHC streams, Engram at layer 1."""
+    c = ModelConfig(
+        arch="deepseek_v4", vocab_size=4096, hidden_size=1024, intermediate_size=2048, moe_intermediate_size=256,
+        num_hidden_layers=4, first_k_dense_replace=1, num_attention_heads=16, q_lora_rank=384, kv_lora_rank=512,
+        qk_nope_head_dim=448, qk_rope_head_dim=64, v_head_dim=512, o_lora_rank=512, o_groups=4, attn_sink=True,
+        n_routed_experts=32, n_shared_experts=1, num_experts_per_tok=6, n_group=1, topk_group=1,
+        routed_scaling_factor=1.5, scoring_func="sqrtsoftplus", prune_budget=0.4, prune_max_count=1,
+        hc_mult=4, hc_sinkhorn_iters=20, engram_layers=(1,), engram_heads=8, engram_dim=256, engram_rows=8192,
+        aux_layers=(3,), max_position_embeddings=8192, rope_scaling=None)
+    return dataclasses.replace(c, **over)
+
+
+def v41_flash_config(**over) -> ModelConfig:
+    """DeepSeek-V4.1-Flash-shaped decoder (the reference's served model, facts
+    from its kernel constants): hidden 5120, 40 layers, 64 MQA heads of 512
+    (rope tail 64), q_lora 1280, 8 output groups of rank 1024, 384 routed
+    experts top-6 (sqrt-softplus, E5 prune 0.4) + 1 shared, 4 mHC streams,
+    Engram at layers 1 and 14 (100 hash heads of 256).  Widths the reference
+    does not pin (expert width 2304 from its shared expert, vocab, table
+    rows) are stated here."""
+    c = ModelConfig(
+        arch="deepseek_v4", vocab_size=129280, hidden_size=5120, intermediate_size=12288,
+        moe_intermediate_size=2304, num_hidden_layers=40, first_k_dense_replace=0, num_attention_heads=64,
+        q_lora_rank=1280, kv_lora_rank=512, qk_nope_head_dim=448, qk_rope_head_dim=64, v_head_dim=512,
+        o_lora_rank=1024, o_groups=8, attn_sink=True, n_routed_experts=384, n_shared_experts=1,
+        num_experts_per_tok=6, n_group=1, topk_group=1, routed_scaling_factor=2.5, scoring_func="sqrtsoftplus",
+        prune_budget=0.4, prune_max_count=1, hc_mult=4, hc_sinkhorn_iters=20, engram_layers=(1, 14),
+        engram_heads=100, engram_dim=256, engram_rows=1 << 22, aux_layers=(37, 38, 39),
+        max_position_embeddings=163840, rope_scaling=None, expert_format="nvfp4")
+    return dataclasses.replace(c, **over)
+
+
 PRESETS = {
     "tiny": tiny_config,
     "deepseek-v3-671b": v3_671b_config,
     "deepseek-v3.2-sparse-671b": v32_sparse_config,
     "deepseek-v3-671b-nvfp4": v3_nvfp4_config,
     "small": small_gpu_config,
+    "tiny-v4": tiny_v4_config,
+    "small-v4": small_v4_gpu_config,
+    "deepseek-v4.1-flash": v41_flash_config,
 }
 
 

@@ -1,0 +1,281 @@
+"""DeepSeek-V4-family decoder for the serving engine (arch="deepseek_v4").
+
+Per token the residual state is hc streams X [hc, D] (bf16 on the GPU).  Each
+sublayer (attention, then FFN) runs three kernels around its body:
+  * hc_post (previous sublayer): X <- post * y + comb^T X, with the sum of
+    squares of the new streams (the RMS of the coefficients);
+  * the stats GEMM on the tensor cores: raw = X_flat . fn^T with fn split in
+    bf16 hi / mid / lo parts (split-K, fp32 accumulation);
+  * hc_pre: pre / post / comb (row softmax + Sinkhorn on 16 lanes) and the
+    sublayer input RMSNorm(sum_c pre_c X_c) * w as the next GEMM's MXFP8
+    operand.
+Attention is MQA over one latent row per token (K = V, RoPE on its tail)
+through the tcgen05 latent-attention kernel, with per-head sinks and the
+inverse RoPE of the output tail in one fix-up kernel; the output projection
+is the grouped low-rank wo_a on the bf16 tensor-core batched GEMM (its
+epilogue writes wo_b's MXFP8 operand) then wo_b.  MoE: sqrt-softplus router
+(+ E5 prune at decode) into the fused expert kernels.  Engram layers gate
+hashed host-table rows into every stream before their attention.
+
+Parallelism: TP over heads / output groups / FFN columns with an all-reduce
+after each sublayer, routed experts EP-split over the same ranks (one
+all-reduce for routed + shared), Engram tables row-sharded (zeros for rows
+owned elsewhere, summed by the all-reduce), vocab-parallel LM head.
+
+Reference parity: fork_loop.py:59-226 (layer loop with hc_broadcast /
+hc_combine head), hq_layer.py:32-101 / fg_layer.py (hyper-connection
+sublayers), fork_attn.py:380-553 (MQA, sinks, inverse rope, wo_a / wo_b),
+moe_fwd.py:67-263 (MoE), eg.py:355-390 (Engram), aux.py (stream means).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Dict, List, Optional
+
+import torch
+
+from .. import ops
+from ..config import EngineConfig, ModelConfig
+from ..ops import EngramWeights, HcWeights
+from ..parallel.state import ParallelState
+from .batch import ForwardBatch
+from .deepseek import DenseWeights, Linear, MoEWeights
+from .rope import cos_sin_table
+
+
+@dataclass
+class V4AttnWeights:
+    wqkv_a: Linear                # [q_lora + L, D]
+    q_norm: torch.Tensor
+    kv_norm: torch.Tensor
+    wq_b: Linear                  # [Hl * L, q_lora]
+    wo_a: torch.Tensor            # [Gl, R, (H/G) * L]
+    wo_b: Linear                  # [D, Gl * R]
+    sink: Optional[torch.Tensor]  # [Hl]
+
+
+@dataclass
+class V4LayerWeights:
+    attn_hc: HcWeights
+    ffn_hc: HcWeights
+    in_ln: torch.Tensor
+    post_ln: torch.Tensor
+    attn: V4AttnWeights
+    ffn: object                   # DenseWeights | MoEWeights
+    engram: Optional[EngramWeights] = None
+
+
+class DeepseekV4Model:
+    def __init__(self, cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState, layers: List[V4LayerWeights],
+                 embed: torch.Tensor, hc_head: HcWeights, final_ln: torch.Tensor, lm_head, device,
+                 kv_dtype=torch.float8_e4m3fn):
+        assert cfg.is_v4 and cfg.hc_mult > 0
+        self.cfg, self.ecfg, self.ps = cfg, ecfg, ps
+        self.layers = layers
+        self.embed = embed
+        self.hc_head = hc_head
+        self.final_ln = final_ln
+        self.lm_head = lm_head
+        self.device = torch.device(device)
+        self.kv_dtype = kv_dtype
+        self.heads = cfg.num_attention_heads // ps.tp_size
+        self.groups = cfg.o_groups // ps.tp_size
+        self.rope_table = cos_sin_table(cfg, cfg.max_position_embeddings, device=self.device)
+        self.kv_scale = [1.0] * len(layers)
+        self.kv_cache: List[torch.Tensor] = []
+        self.tok_cache: Optional[torch.Tensor] = None
+        self.page_size = ecfg.page_size
+        self.aux: List[torch.Tensor] = []
+        from ..ops.ref import engram_multipliers
+        m = [v - (1 << 64) if v >= (1 << 63) else v for v in engram_multipliers(max(cfg.engram_heads, 1))]
+        self.engram_mults = torch.tensor(m, dtype=torch.int64, device=self.device)
+
+    # ------------------------------------------------------------------
+    def allocate_kv(self, num_pages: int):
+        c = self.cfg
+        slots = num_pages * self.page_size
+        self.kv_cache = [torch.zeros(slots, c.kv_cache_dim, dtype=self.kv_dtype, device=self.device)
+                         for _ in self.layers]
+        if c.engram_layers:
+            self.tok_cache = torch.full((slots,), -1, dtype=torch.int32, device=self.device)
+
+    def kv_bytes_per_token(self) -> int:
+        per = self.cfg.kv_cache_dim * torch.tensor([], dtype=self.kv_dtype).element_size()
+        return per * len(self.layers) + (4 if self.cfg.engram_layers else 0)
+
+    def vocab_offset(self) -> int:
+        rows = getattr(self.lm_head, "rows", None)
+        n = rows if rows is not None else self.lm_head.shape[0]
+        return self.ps.tp_rank * n
+
+    # ------------------------------------------------------------------
+    def _out_dtype(self):
+        return torch.float32 if self.device.type == "cpu" else torch.bfloat16
+
+    def _reduce(self, y: torch.Tensor) -> torch.Tensor:
+        if self.ps.tp_size > 1:
+            self.ps.tp_all_reduce(y)
+        elif self.ps.ep_size > 1:
+            self.ps.ep_all_reduce(y)
+        return y
+
+    def _attention(self, i: int, lw: V4LayerWeights, h, fb: ForwardBatch) -> torch.Tensor:
+        c = self.cfg
+        aw = lw.attn
+        T = fb.num_tokens
+        L, rd, ql = c.kv_lora_rank, c.qk_rope_head_dim, c.q_lora_rank
+        od = self._out_dtype()
+        qkv = aw.wqkv_a(h, out_dtype=od)
+        q_lat = ops.rmsnorm_act(qkv[:, :ql], aw.q_norm, c.rms_norm_eps, aw.wq_b, keep_hf=False)
+        ops.kv_store_v4(qkv[:, ql:ql + L], aw.kv_norm, c.rms_norm_eps, self.rope_table, fb.positions,
+                        self.kv_cache[i], fb.out_slots, self.kv_scale[i], rd)
+        q = aw.wq_b(q_lat, out_dtype=od).view(T, self.heads, L)
+        o = ops.mqa_attention(q, self.kv_cache[i], self.kv_scale[i], fb, c.softmax_scale, self.page_size, aw.sink,
+                              self.rope_table, rd)
+        z = ops.absorb_o(o.reshape(T, self.groups, -1), aw.wo_a, quantize=aw.wo_b.quantized)
+        y = aw.wo_b(z, out_dtype=od)
+        return self._reduce(y)
+
+    def _ffn(self, i: int, lw: V4LayerWeights, h, fb: ForwardBatch) -> torch.Tensor:
+        c = self.cfg
+        od = self._out_dtype()
+        if isinstance(lw.ffn, DenseWeights):
+            return self._reduce(lw.ffn.down(ops.gate_up_swiglu(h, lw.ffn.gate_up), out_dtype=od))
+        mw: MoEWeights = lw.ffn
+        w, ids = ops.router(h, mw.gate, mw.bias, c)
+        if fb.is_decode and c.prune_budget > 0:
+            w, ids = ops.e5_prune(w, ids, c, c.n_routed_experts)
+        out = ops.moe_experts(h, w, ids, mw.experts, out_dtype=od, n_experts_total=c.n_routed_experts)
+        if mw.shared_gate_up is not None:
+            out = out + mw.shared_down(ops.gate_up_swiglu(h, mw.shared_gate_up), out_dtype=od)
+        return self._reduce(out.to(od))
+
+    def _ffn_first_linear(self, lw: V4LayerWeights):
+        if isinstance(lw.ffn, DenseWeights):
+            return lw.ffn.gate_up
+        return lw.ffn.shared_gate_up
+
+    def _hidden(self, fb: ForwardBatch):
+        c = self.cfg
+        eps = c.rms_norm_eps
+        X, ss = ops.hc_embed(self.embed, fb.input_ids, c.hc_mult)
+        eids = None
+        if c.engram_layers:
+            eids = ops.engram_ids(fb, self.tok_cache, c, self.engram_mults, self.page_size)
+        self.aux = []
+        carry = None
+        for i, lw in enumerate(self.layers):
+            if carry is not None:
+                ss = ops.hc_post(X, *carry)
+            if lw.engram is not None:
+                ss = ops.engram_update(X, eids, lw.engram, c, self.ps)
+            if i in c.aux_layers:
+                self.aux.append(ops.hc_mean(X))
+            h, post, comb = ops.hc_pre(X, ss, lw.attn_hc, lw.in_ln, eps, c, lw.attn.wqkv_a)
+            y = self._attention(i, lw, h, fb)
+            ss = ops.hc_post(X, y, post, comb)
+            moe = isinstance(lw.ffn, MoEWeights)
+            h, post, comb = ops.hc_pre(X, ss, lw.ffn_hc, lw.post_ln, eps, c, self._ffn_first_linear(lw),
+                                       keep_hf=moe)
+            carry = (self._ffn(i, lw, h, fb), post, comb)
+        ss = ops.hc_post(X, *carry)
+        h, _, _ = ops.hc_pre(X, ss, self.hc_head, self.final_ln, eps, c, None, head=True)
+        return h
+
+    def _last_hidden(self, h, fb: ForwardBatch) -> torch.Tensor:
+        x = ops.to_float(h)
+        if x.is_cuda:
+            x = x.to(torch.bfloat16)
+        if fb.is_decode and int(fb.last_idx.shape[0]) == int(x.shape[0]):
+            return x
+        return x[fb.last_idx]
+
+    @torch.no_grad()
+    def forward(self, fb: ForwardBatch) -> torch.Tensor:
+        """Logits [B, V] (full vocab) of each sequence's last token."""
+        h = self._hidden(fb)
+        return ops.lm_head_logits(self._last_hidden(h, fb), self.lm_head, self.ps)
+
+    @torch.no_grad()
+    def forward_tokens(self, fb: ForwardBatch, temperature, top_p, top_k, uniform) -> torch.Tensor:
+        h = self._hidden(fb)
+        local = ops.lm_head_local(self._last_hidden(h, fb), self.lm_head)
+        return ops.sample_tokens(local, self.vocab_offset(), temperature, top_p, top_k, uniform, self.ps)
+
+
+# ---------------------------------------------------------------------------
+# construction from a full state dict (names of models/reference_v4.py)
+# ---------------------------------------------------------------------------
+
+def build_model_v4(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState, sd: Dict[str, torch.Tensor],
+                   device="cpu", kv_dtype=None) -> DeepseekV4Model:
+    """This rank's V4 model from a FULL (unsharded) fp32 state dict:
+
+      model.embed_tokens.weight, model.norm.weight, lm_head.weight,
+      model.hc_head.{fn, scale, base},
+      model.layers.i.{attn_hc, ffn_hc}.{fn, scale, base},
+      model.layers.i.{input_layernorm, post_attention_layernorm}.weight,
+      model.layers.i.self_attn.{wqkv_a, wq_b, wo_a, wo_b}.weight,
+        .{q_norm, kv_norm}.weight, .attn_sink,
+      model.layers.i.mlp.* (DeepSeek-V3 names),
+      model.layers.i.engram.{table, table_scale, wkv.weight, q_norm.weight,
+        k_norm.weight}.
+    """
+    from .loader import _quantize, build_ffn
+    assert not ecfg.dp_attention, "DeepSeek-V4 family: TP attention + EP experts"
+    dev = torch.device(device)
+    tp, tr = ps.tp_size, ps.tp_rank
+    H, L, G, R = cfg.num_attention_heads, cfg.kv_lora_rank, cfg.o_groups, cfg.o_lora_rank
+    assert H % tp == 0 and G % tp == 0 and H % G == 0
+    Hl, Gl = H // tp, G // tp
+    fmt_d = cfg.dense_format
+    wdt = torch.bfloat16 if dev.type == "cuda" else torch.float32
+
+    def get(name) -> torch.Tensor:
+        return sd[name].float()
+
+    def split(t, dim, n, r):
+        return t.chunk(n, dim)[r].contiguous() if n > 1 else t
+
+    def hcw(prefix) -> HcWeights:
+        return HcWeights(get(prefix + "fn").to(dev).contiguous(), get(prefix + "scale").to(dev),
+                         get(prefix + "base").to(dev))
+
+    layers: List[V4LayerWeights] = []
+    for i in range(cfg.num_hidden_layers):
+        p = f"model.layers.{i}."
+        a = p + "self_attn."
+        wq_b = split(get(a + "wq_b.weight").view(H, L, -1), 0, tp, tr).reshape(Hl * L, -1)
+        wo_a = split(get(a + "wo_a.weight").view(G, R, -1), 0, tp, tr).to(dev, wdt).contiguous()
+        wo_b = split(get(a + "wo_b.weight"), 1, tp, tr)
+        sink = split(get(a + "attn_sink"), 0, tp, tr).to(dev).contiguous() if cfg.attn_sink else None
+        aw = V4AttnWeights(wqkv_a=Linear(_quantize(get(a + "wqkv_a.weight"), fmt_d, dev)),
+                           q_norm=get(a + "q_norm.weight").to(dev), kv_norm=get(a + "kv_norm.weight").to(dev),
+                           wq_b=Linear(_quantize(wq_b, fmt_d, dev)), wo_a=wo_a,
+                           wo_b=Linear(_quantize(wo_b, fmt_d, dev)), sink=sink)
+        eng = None
+        if i in cfg.engram_layers:
+            e = p + "engram."
+            table, scale = sd[e + "table"], sd[e + "table_scale"]
+            rows = table.shape[0]
+            lo, hi = tr * rows // tp, (tr + 1) * rows // tp
+            t_sh, s_sh = table[lo:hi].contiguous(), scale[lo:hi].contiguous()
+            if dev.type == "cuda":
+                # host-resident tables, read by the gather kernel through their device mapping
+                t_sh, s_sh = t_sh.pin_memory(), s_sh.pin_memory()
+            eng = EngramWeights(table=t_sh, scale=s_sh, row_lo=lo,
+                                wkv=Linear(_quantize(get(e + "wkv.weight"), fmt_d, dev)),
+                                q_w=get(e + "q_norm.weight").to(dev), k_w=get(e + "k_norm.weight").to(dev))
+        layers.append(V4LayerWeights(attn_hc=hcw(p + "attn_hc."), ffn_hc=hcw(p + "ffn_hc."),
+                                     in_ln=get(p + "input_layernorm.weight").to(dev),
+                                     post_ln=get(p + "post_attention_layernorm.weight").to(dev), attn=aw,
+                                     ffn=build_ffn(cfg, sd, get, split, p + "mlp.", i, ps, dev), engram=eng))
+    emb_dt = torch.bfloat16 if dev.type == "cuda" else torch.float32
+    embed = get("model.embed_tokens.weight").to(dev, emb_dt).contiguous()
+    head_full = sd["model.embed_tokens.weight"] if cfg.tie_word_embeddings else sd["lm_head.weight"]
+    head = split(head_full.float(), 0, tp, tr)
+    head = _quantize(head, "mxfp8", dev) if fmt_d == "mxfp8" and dev.type == "cuda" else head.to(dev, emb_dt)
+    if kv_dtype is None:
+        kv_dtype = torch.float8_e4m3fn if dev.type == "cuda" else torch.float32
+    return DeepseekV4Model(cfg, ecfg, ps, layers, embed, hcw("model.hc_head."), get("model.norm.weight").to(dev),
+                           head, dev, kv_dtype=kv_dtype)

@@ -68,6 +68,41 @@ def _maybe_tile(ex: ExpertWeights) -> ExpertWeights:
     return ex
 
 
+def build_ffn(cfg: ModelConfig, sd, get, split, m: str, i: int, ps: ParallelState, dev):
+    """Layer i's FFN from the state dict: routed experts (this rank's EP
+    slice, stacked in the expert format) + TP-split shared expert, or the
+    TP-split dense SwiGLU FFN."""
+    fmt_d = cfg.dense_format
+    tp, tr = ps.tp_size, ps.tp_rank
+    if cfg.is_moe_layer(i):
+        per = cfg.n_routed_experts // ps.ep_size
+        first = ps.ep_rank * per
+        w13, w2 = [], []
+        for e in range(first, first + per):
+            q = m + f"experts.{e}."
+            w13.append(_quantize(torch.cat([get(q + "gate_proj.weight"), get(q + "up_proj.weight")], 0),
+                                 cfg.expert_format, dev))
+            w2.append(_quantize(get(q + "down_proj.weight"), cfg.expert_format, dev))
+        ex = _maybe_tile(ExpertWeights(first=first, count=per, w13=_stack(w13), w2=_stack(w2),
+                                       inter=cfg.moe_intermediate_size))
+        sgu = sdn = None
+        if cfg.n_shared_experts:
+            q = m + "shared_experts."
+            g = split(get(q + "gate_proj.weight"), 0, tp, tr)
+            u = split(get(q + "up_proj.weight"), 0, tp, tr)
+            sgu = Linear(_quantize(torch.cat([g, u], 0), fmt_d, dev))
+            sdn = Linear(_quantize(split(get(q + "down_proj.weight"), 1, tp, tr), fmt_d, dev))
+        ffn = MoEWeights(gate=get(m + "gate.weight").to(dev),
+                         bias=sd[m + "gate.e_score_correction_bias"].float().to(dev),
+                         experts=ex, shared_gate_up=sgu, shared_down=sdn)
+    else:
+        g = split(get(m + "gate_proj.weight"), 0, tp, tr)
+        u = split(get(m + "up_proj.weight"), 0, tp, tr)
+        ffn = DenseWeights(gate_up=Linear(_quantize(torch.cat([g, u], 0), fmt_d, dev)),
+                           down=Linear(_quantize(split(get(m + "down_proj.weight"), 1, tp, tr), fmt_d, dev)))
+    return ffn
+
+
 def build_model(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState,
                 sd: Dict[str, torch.Tensor], device="cpu", kv_dtype=None) -> DeepseekModel:
     """Build this rank's model from a FULL (unsharded) HF-named state dict of
@@ -121,33 +156,7 @@ def build_model(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState,
             ix = a + "indexer."
             aw.ix_k_norm_w = sd[ix + "k_norm.weight"].float().to(dev)
             aw.ix_k_norm_b = sd[ix + "k_norm.bias"].float().to(dev)
-        m = p + "mlp."
-        if cfg.is_moe_layer(i):
-            per = cfg.n_routed_experts // ps.ep_size
-            first = ps.ep_rank * per
-            w13, w2 = [], []
-            for e in range(first, first + per):
-                q = m + f"experts.{e}."
-                w13.append(_quantize(torch.cat([get(q + "gate_proj.weight"), get(q + "up_proj.weight")], 0),
-                                     cfg.expert_format, dev))
-                w2.append(_quantize(get(q + "down_proj.weight"), cfg.expert_format, dev))
-            ex = _maybe_tile(ExpertWeights(first=first, count=per, w13=_stack(w13), w2=_stack(w2),
-                                           inter=cfg.moe_intermediate_size))
-            sgu = sdn = None
-            if cfg.n_shared_experts:
-                q = m + "shared_experts."
-                g = split(get(q + "gate_proj.weight"), 0, tp, tr)
-                u = split(get(q + "up_proj.weight"), 0, tp, tr)
-                sgu = Linear(_quantize(torch.cat([g, u], 0), fmt_d, dev))
-                sdn = Linear(_quantize(split(get(q + "down_proj.weight"), 1, tp, tr), fmt_d, dev))
-            ffn = MoEWeights(gate=get(m + "gate.weight").to(dev),
-                             bias=sd[m + "gate.e_score_correction_bias"].float().to(dev),
-                             experts=ex, shared_gate_up=sgu, shared_down=sdn)
-        else:
-            g = split(get(m + "gate_proj.weight"), 0, tp, tr)
-            u = split(get(m + "up_proj.weight"), 0, tp, tr)
-            ffn = DenseWeights(gate_up=Linear(_quantize(torch.cat([g, u], 0), fmt_d, dev)),
-                               down=Linear(_quantize(split(get(m + "down_proj.weight"), 1, tp, tr), fmt_d, dev)))
+        ffn = build_ffn(cfg, sd, get, split, p + "mlp.", i, ps, dev)
         layers.append(LayerWeights(in_ln=sd[p + "input_layernorm.weight"].float().to(dev),
                                    post_ln=sd[p + "post_attention_layernorm.weight"].float().to(dev),
                                    attn=aw, ffn=ffn))

@@ -258,7 +258,7 @@ def absorb_o(o_lat: torch.Tensor, w_uv: torch.Tensor, quantize: bool = False):
     (quantized straight from the head-major batched-GEMM output)."""
     T, H, L = o_lat.shape
     if o_lat.is_cuda:
-        if (quantize and _IMPL == "native" and w_uv.dtype == torch.bfloat16 and w_uv.shape[1] == 128
+        if (quantize and _IMPL == "native" and w_uv.dtype == torch.bfloat16 and w_uv.shape[1] % 128 == 0
                 and o_lat.dtype == torch.bfloat16):
             return _native().absorb_o_mx(o_lat, w_uv.contiguous())
         y = torch.bmm(o_lat.transpose(0, 1).to(w_uv.dtype), w_uv.transpose(1, 2))      # [H, T, v]
@@ -340,6 +340,8 @@ def router(h, gate: torch.Tensor, bias: torch.Tensor, cfg):
     if _use_native(x):
         return _native().router(x, gate, bias, cfg)
     logits = x.float() @ gate.float().T
+    if cfg.scoring_func == "sqrtsoftplus":
+        return ref.router_sqrtsoftplus(logits, bias, cfg.num_experts_per_tok, cfg.routed_scaling_factor)
     return ref.router_topk(logits, bias, cfg.num_experts_per_tok, cfg.n_group, cfg.topk_group,
                            cfg.routed_scaling_factor, cfg.norm_topk_prob)
 
@@ -450,3 +452,167 @@ def sample(logits: torch.Tensor, temperature, top_p, top_k, uniform) -> torch.Te
     if _use_native(logits):
         return _native().sample(logits, temperature, top_p, top_k, uniform)
     return ref.sample(logits, temperature, top_p, top_k, uniform)
+
+
+# ---------------------------------------------------------------------------
+# DeepSeek-V4 family: mHC residual streams, MQA with sinks, E5, Engram
+# ---------------------------------------------------------------------------
+
+@dataclass
+class HcWeights:
+    """Coefficient weights of one hyper-connection (a sublayer's or the
+    head's): fn [M, hc*D] fp32, scale [3] (sublayer) or [1] (head), base [M].
+    fn_parts (GPU): [128, hc*D] bf16 holding fn as hi / mid / lo bf16 parts
+    (rows p*M + j), the weight operand of the tcgen05 stats GEMM."""
+    fn: torch.Tensor
+    scale: torch.Tensor
+    base: torch.Tensor
+    fn_parts: Optional[torch.Tensor] = None
+
+    @property
+    def m(self) -> int:
+        return self.fn.shape[0]
+
+
+@dataclass
+class EngramWeights:
+    """Engram table shard (rows [row_lo, row_lo + rows) of the layer's
+    table, e4m3 bytes [rows, dim] + UE8M0 [rows, dim/32], in pinned host
+    memory on GPU ranks), the kv projection and the gate norms."""
+    table: torch.Tensor
+    scale: torch.Tensor
+    row_lo: int
+    wkv: object            # Linear [2D, heads*dim]
+    q_w: torch.Tensor
+    k_w: torch.Tensor
+
+
+def hc_embed(embed: torch.Tensor, ids: torch.Tensor, hc: int):
+    """Residual streams of the first layer: every stream = the token's
+    embedding row.  Returns (X [T, hc, D], sum of squares [T])."""
+    if _use_native(embed):
+        return _native().hc_embed(embed, ids, hc)
+    e = embed[ids.long()].float()
+    X = e.unsqueeze(1).expand(-1, hc, -1).contiguous()
+    return X, X.pow(2).sum((1, 2))
+
+
+def hc_post(X: torch.Tensor, y: torch.Tensor, post: torch.Tensor, comb: torch.Tensor) -> torch.Tensor:
+    """X <- post * y + comb^T X (in place); returns the new sum of squares [T]."""
+    if _use_native(X):
+        return _native().hc_post(X, y, post, comb)
+    hc = X.shape[1]
+    out = ref.hc_post(X, y, post, comb.reshape(-1, hc, hc))
+    X.copy_(out)
+    return out.pow(2).sum((1, 2))
+
+
+def hc_pre(X: torch.Tensor, sumsq: torch.Tensor, hw: HcWeights, norm_w: torch.Tensor, eps: float, cfg,
+           next_linear=None, head: bool = False, keep_hf: bool = False):
+    """Sublayer coefficients from the streams and the sublayer input
+    RMSNorm(sum_c pre_c X_c) * norm_w in the operand format of next_linear.
+    Returns (h, post, comb) (head=True: post and comb are None)."""
+    if _use_native(X):
+        return _native().hc_pre(X, sumsq, hw, norm_w, eps, cfg, next_linear, head, keep_hf)
+    hc, D = X.shape[1], X.shape[2]
+    raw = X.float().flatten(1) @ hw.fn.float().T
+    if head:
+        pre = ref.hc_head_coeffs(raw, sumsq, hw.scale, hw.base, hc, hc * D, cfg.hc_eps)
+        post = comb = None
+    else:
+        pre, post, comb = ref.hc_coeffs(raw, sumsq, hw.scale, hw.base, hc, hc * D, cfg.hc_sinkhorn_iters,
+                                        cfg.hc_eps)
+        comb = comb.reshape(-1, hc * hc)
+    x = ref.hc_combine(X, pre)
+    if X.is_cuda:
+        x = x.to(torch.bfloat16)
+    return rmsnorm_act(x, norm_w, eps, next_linear, keep_hf), post, comb
+
+
+def hc_mean(X: torch.Tensor) -> torch.Tensor:
+    if _use_native(X):
+        return _native().hc_mean(X)
+    return X.float().mean(1)
+
+
+def kv_store_v4(kv: torch.Tensor, w: torch.Tensor, eps: float, table: torch.Tensor, pos: torch.Tensor,
+                cache: torch.Tensor, slots: torch.Tensor, kv_scale: float, rd: int) -> None:
+    """cache[slots, :L] = (rmsnorm(kv) with RoPE on its last rd dims) /
+    kv_scale; the row's rope-key part stays zero (K = V = the latent row)."""
+    if _use_native(kv):
+        return _native().kv_store_v4(kv, w, eps, table, pos, cache, slots, kv_scale, rd)
+    L = kv.shape[1]
+    x = ref.rmsnorm(kv, w, eps)
+    x = torch.cat([x[:, :L - rd], ref.rope(x[:, L - rd:], pos, table)], -1)
+    row = torch.zeros(x.shape[0], cache.shape[1], dtype=torch.float32)
+    row[:, :L] = x / kv_scale
+    if cache.dtype == torch.float8_e4m3fn:
+        cache[slots.long()] = row.clamp(-448, 448).to(cache.dtype)
+    else:
+        cache[slots.long()] = row.to(cache.dtype)
+
+
+def mqa_attention(q: torch.Tensor, cache: torch.Tensor, kv_scale: float, fb, softmax_scale: float, page_size: int,
+                  sink: Optional[torch.Tensor], table: torch.Tensor, rd: int, topk=None) -> torch.Tensor:
+    """MQA over the paged latent rows (K = V = row[:L]) with RoPE on the
+    query tails, per-head sinks, and the output tails rotated back to
+    position 0.  q [T, H, L] -> o [T, H, L]."""
+    if _use_native(q):
+        return _native().mqa_attention(q, cache, kv_scale, fb, softmax_scale, page_size, sink, table, rd, topk)
+    T, H, L = q.shape
+    qf = q.float()
+    qf = torch.cat([qf[..., :L - rd], ref.rope(qf[..., L - rd:], fb.positions, table)], -1)
+    o = ref.mqa_sink_attention(qf, cache, kv_scale, fb.block_table, fb.q_seq, fb.positions, softmax_scale, page_size,
+                               sink, L, topk)
+    return ref.inv_rope_tail(o, fb.positions, table, rd)
+
+
+def e5_prune(w: torch.Tensor, ids: torch.Tensor, cfg, n_experts: int):
+    """E5 routed-expert prune of a decode batch (returns new (w, ids))."""
+    if _use_native(ids):
+        return _native().e5_prune(w, ids, cfg, n_experts)
+    return ref.e5_prune(ids, w, cfg.prune_budget, cfg.prune_max_count)
+
+
+def engram_ids(fb, tok_cache: torch.Tensor, cfg, mults: torch.Tensor, page_size: int) -> torch.Tensor:
+    """Hash ids [T, heads] of each token's n-grams (the tokens before this
+    batch come from tok_cache, the token stored at every KV slot, which this
+    call updates with the batch's tokens)."""
+    if _use_native(fb.input_ids):
+        return _native().engram_ids(fb, tok_cache, cfg, mults, page_size)
+    T = fb.num_tokens
+    n = cfg.engram_max_ngram
+    ctx = torch.full((T, n), -1, dtype=torch.int64)
+    ids = fb.input_ids.long()
+    pos, qs = fb.positions.long(), fb.q_seq.long()
+    for t in range(T):
+        p, b = int(pos[t]), int(qs[t])
+        for i in range(n):
+            pp = p - i
+            if pp < 0:
+                continue
+            if i == 0:
+                ctx[t, i] = ids[t]
+            elif t - i >= 0 and int(qs[t - i]) == b and int(pos[t - i]) == pp:
+                ctx[t, i] = ids[t - i]
+            else:
+                page = int(fb.block_table[b, pp // page_size])
+                ctx[t, i] = int(tok_cache[page * page_size + pp % page_size])
+    tok_cache[fb.out_slots.long()] = fb.input_ids.to(tok_cache.dtype)
+    return ref.engram_hash(ctx, cfg.engram_heads, cfg.engram_rows, n)
+
+
+def engram_update(X: torch.Tensor, ids: torch.Tensor, ew: EngramWeights, cfg, ps) -> torch.Tensor:
+    """Gather the hashed rows (this rank's shard; all-reduced over TP), project
+    to [k | v], gate v into every stream (X in place).  Returns the new sum
+    of squares of X [T]."""
+    if _use_native(X):
+        return _native().engram_update(X, ids, ew, cfg, ps)
+    emb = ref.engram_gather(ew.table, ew.scale, ids, ew.row_lo, ew.row_lo + ew.table.shape[0])
+    emb = emb.flatten(1)
+    if ps.tp_size > 1:
+        ps.tp_all_reduce(emb)
+    kv = linear(emb, ew.wkv.w, torch.float32)
+    out = ref.engram_gate(X, kv, ew.q_w, ew.k_w, cfg.rms_norm_eps, cfg.engram_clamp)
+    X.copy_(out)
+    return out.pow(2).sum((1, 2))

@@ -269,7 +269,7 @@ def mla_attention(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size, to
     return _mla_core(q8, qs, cache, kv_scale, fb, softmax_scale, page_size, topk)
 
 
-def _mla_core(q8, qs, cache, kv_scale, fb, softmax_scale, page_size, topk):
+def _mla_core(q8, qs, cache, kv_scale, fb, softmax_scale, page_size, topk, lse_out=None):
     T, H, _ = q8.shape
     L = 512
     dev = q8.device
@@ -284,7 +284,7 @@ def _mla_core(q8, qs, cache, kv_scale, fb, softmax_scale, page_size, topk):
         po = torch.empty(nsplit, T, H, L, dtype=torch.float32, device=dev)
         pl = torch.empty(nsplit, T, H, dtype=torch.float32, device=dev)
     _C.mla_tc(q8, qs, cache.view(torch.uint8), kv_scale, fb.block_table, fb.q_seq, fb.positions, page_size,
-              softmax_scale, nsplit, out, po, pl, topk, mla_hb(H))
+              softmax_scale, nsplit, out, po, pl, topk, mla_hb(H), lse_out=lse_out)
     return out
 
 
@@ -314,7 +314,7 @@ def router(x: torch.Tensor, gate: torch.Tensor, bias: torch.Tensor, cfg):
     w = torch.empty(T, K, dtype=torch.float32, device=x.device)
     ids = torch.empty(T, K, dtype=torch.int32, device=x.device)
     _C.router(logits.contiguous(), bias.float(), cfg.n_group, cfg.topk_group, K, cfg.routed_scaling_factor,
-              cfg.norm_topk_prob, w, ids)
+              cfg.norm_topk_prob, w, ids, scoring=1 if cfg.scoring_func == "sqrtsoftplus" else 0)
     return w, ids
 
 
@@ -679,3 +679,112 @@ def sample(logits, temperature, top_p, top_k, uniform):
     j = torch.searchsorted(c, u).clamp(max=V - 1)
     tok = si.gather(1, j).squeeze(-1)
     return torch.where(greedy, logits.argmax(-1), tok)
+
+
+# ---------------------------------------------------------------------------
+# DeepSeek-V4 family
+# ---------------------------------------------------------------------------
+
+def hc_fn_parts(fn: torch.Tensor) -> torch.Tensor:
+    """fp32 [M, K] -> bf16 [128, K]: rows p*M + j hold the p-th bf16 part of
+    fn[j] (hi, mid, lo: fn = hi + mid + lo to ~24 bits), zero rows after."""
+    M, K = fn.shape
+    assert 3 * M <= 128
+    out = torch.zeros(128, K, dtype=torch.bfloat16, device=fn.device)
+    rest = fn.float()
+    for p in range(3):
+        part = rest.to(torch.bfloat16)
+        out[p * M:(p + 1) * M] = part
+        rest = rest - part.float()
+    return out
+
+
+def hc_embed(embed, ids, hc):
+    T, D = ids.shape[0], embed.shape[1]
+    X = torch.empty(T, hc, D, dtype=torch.bfloat16, device=embed.device)
+    ss = torch.empty(T, dtype=torch.float32, device=embed.device)
+    _C.hc_embed(embed, ids.int() if ids.dtype != torch.int32 else ids, X, ss)
+    return X, ss
+
+
+def hc_post(X, y, post, comb):
+    ss = torch.empty(X.shape[0], dtype=torch.float32, device=X.device)
+    yb = y if y.dtype == torch.bfloat16 else y.to(torch.bfloat16)
+    _C.hc_post(X, yb, post, comb, ss)
+    return ss
+
+
+def hc_pre(X, sumsq, hw, norm_w, eps, cfg, next_linear, head, keep_hf):
+    T, hc, D = X.shape
+    K = hc * D
+    parts = hw.fn_parts
+    if parts is None:
+        parts = hw.fn_parts = hc_fn_parts(hw.fn)
+    raw = torch.zeros(T, 128, dtype=torch.float32, device=X.device)
+    splits = max(1, min(32, (K // 64) // 4, 148 // max(1, -(-T // 128))))
+    _C.bf16_absorb(parts.view(1, 128, K), X.view(T, 1, K), 3, raw.view(T, 1, 128), None, None, None, None, None,
+                   None, None, splits=splits)
+    quantized = next_linear is not None and getattr(next_linear, "quantized", False)
+    post = comb = None
+    if not head:
+        post = torch.empty(T, hc, dtype=torch.float32, device=X.device)
+        comb = torch.empty(T, hc * hc, dtype=torch.float32, device=X.device)
+    a = alloc_qact(T, D, X.device) if quantized else None
+    hb = torch.empty(T, D, dtype=torch.bfloat16, device=X.device) if (keep_hf or not quantized) else None
+    _C.hc_pre(raw, 3, hw.m, sumsq, hw.scale, hw.base, 1 if head else 0, cfg.hc_sinkhorn_iters, cfg.hc_eps, X,
+              norm_w, eps, post, comb, a.q if a else None, a.sf if a else None, hb, None)
+    if a is not None:
+        a.hf = hb
+        return a, post, comb
+    return hb, post, comb
+
+
+def hc_mean(X):
+    out = torch.empty(X.shape[0], X.shape[2], dtype=torch.bfloat16, device=X.device)
+    _C.hc_mean(X, out)
+    return out
+
+
+def kv_store_v4(kv, w, eps, table, pos, cache, slots, kv_scale, rd):
+    _C.kv_store_v4(kv, w, eps, pos, table, cache.view(torch.uint8), slots, kv_scale, rd)
+
+
+def mqa_attention(q, cache, kv_scale, fb, softmax_scale, page_size, sink, table, rd, topk=None):
+    T, H, L = q.shape
+    dev = q.device
+    q8 = torch.empty(T, H, 576, dtype=torch.uint8, device=dev)
+    qs = torch.empty(T, H, dtype=torch.float32, device=dev)
+    qb = q if q.dtype == torch.bfloat16 else q.to(torch.bfloat16)
+    _C.mqa_q_prep(qb, fb.positions, table, rd, q8, qs)
+    lse = torch.empty(T, H, dtype=torch.float32, device=dev) if sink is not None else None
+    out = _mla_core(q8, qs, cache, kv_scale, fb, softmax_scale, page_size, topk, lse_out=lse)
+    _C.attn_fixup(out, lse, sink, rd, fb.positions, table)
+    return out
+
+
+def e5_prune(w, ids, cfg, n_experts):
+    w = w.contiguous()
+    ids = ids.contiguous()
+    _C.e5_prune(ids, w, n_experts, cfg.prune_budget, cfg.prune_max_count)
+    return w, ids
+
+
+def engram_ids(fb, tok_cache, cfg, mults, page_size):
+    out = torch.empty(fb.num_tokens, cfg.engram_heads, dtype=torch.int32, device=fb.input_ids.device)
+    _C.engram_hash(fb.input_ids, fb.positions, fb.q_seq, fb.block_table, fb.out_slots, page_size, tok_cache,
+                   cfg.engram_heads, cfg.engram_rows, cfg.engram_max_ngram, mults, out)
+    return out
+
+
+def engram_update(X, ids, ew, cfg, ps):
+    T = X.shape[0]
+    nh = ids.shape[1]
+    emb = torch.empty(T, nh * 256, dtype=torch.bfloat16, device=X.device)
+    _C.engram_gather(ew.table, ew.scale, ids.contiguous(), ew.row_lo, emb)
+    if ps.tp_size > 1:
+        ps.tp_all_reduce(emb)
+    from . import linear
+    kv = linear(emb, ew.wkv.w, torch.bfloat16)
+    ss = torch.empty(T, dtype=torch.float32, device=X.device)
+    _C.engram_gate(X, kv, ew.q_w, ew.k_w, cfg.rms_norm_eps, cfg.engram_clamp, ss)
+    return ss

@@ -172,3 +172,216 @@ def sample(logits: torch.Tensor, temperature: torch.Tensor, top_p: torch.Tensor,
         j = int(torch.searchsorted(c, torch.tensor([u], device=c.device)).clamp(max=V - 1))
         out[i] = si[j]
     return out
+
+
+# -- DeepSeek-V4 family ------------------------------------------------------------------
+# mHC (hyper-connections over hc residual streams), sqrt-softplus routing with
+# the E5 prune, MQA attention with sinks, Engram lookups.  Reference parity:
+# sk_unit.cu:1-15 (coefficient epilogue: sigmoid pre / 2*sigmoid post,
+# row-softmax + Sinkhorn comb), fin.py:218-246 (post: out_c = post_c * y +
+# sum_r comb[r][c] * x_r), route_e5.cu:4-12 (sqrt-softplus top-k, E5 prune),
+# eg_gather.cu:1-5 (e4m3 rows x 2^(e-127)).
+
+def hc_stats(X: torch.Tensor, fn: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """X [T, hc, D] -> (raw mixes [T, M] = X_flat . fn^T, sum of squares [T])."""
+    xf = X.float().flatten(1)
+    return xf @ fn.float().T, xf.pow(2).sum(-1)
+
+
+def sinkhorn(c: torch.Tensor, iters: int, eps: float) -> torch.Tensor:
+    """[.., n, n] logits -> row softmax (+eps), then column / row
+    normalisations (each sum + eps) ending on columns: iters column passes."""
+    m = c.float().softmax(-1) + eps
+    m = m / (m.sum(-2, keepdim=True) + eps)
+    for _ in range(iters - 1):
+        m = m / (m.sum(-1, keepdim=True) + eps)
+        m = m / (m.sum(-2, keepdim=True) + eps)
+    return m
+
+
+def hc_coeffs(raw: torch.Tensor, sumsq: torch.Tensor, scale: torch.Tensor, base: torch.Tensor, hc: int,
+              width: int, iters: int, eps: float):
+    """Sublayer coefficients from the raw mixes: (pre [T,hc], post [T,hc],
+    comb [T,hc,hc]); width = hc * hidden (the RMS divisor)."""
+    r = torch.rsqrt(sumsq.float() / width + eps).unsqueeze(-1)
+    s = scale.float()
+    b = base.float()
+    pre = torch.sigmoid(s[0] * r * raw[:, :hc] + b[:hc]) + eps
+    post = 2.0 * torch.sigmoid(s[1] * r * raw[:, hc:2 * hc] + b[hc:2 * hc])
+    c = (s[2] * r * raw[:, 2 * hc:2 * hc + hc * hc] + b[2 * hc:]).view(-1, hc, hc)
+    return pre, post, sinkhorn(c, iters, eps)
+
+
+def hc_head_coeffs(raw: torch.Tensor, sumsq: torch.Tensor, scale: torch.Tensor, base: torch.Tensor, hc: int,
+                   width: int, eps: float) -> torch.Tensor:
+    r = torch.rsqrt(sumsq.float() / width + eps).unsqueeze(-1)
+    return torch.sigmoid(scale.float()[0] * r * raw[:, :hc] + base.float()[:hc]) + eps
+
+
+def hc_combine(X: torch.Tensor, pre: torch.Tensor) -> torch.Tensor:
+    return (pre.float().unsqueeze(-1) * X.float()).sum(1)
+
+
+def hc_post(X: torch.Tensor, y: torch.Tensor, post: torch.Tensor, comb: torch.Tensor) -> torch.Tensor:
+    """out[:, c] = post[:, c] * y + sum_r comb[:, r, c] * X[:, r]."""
+    return post.float().unsqueeze(-1) * y.float().unsqueeze(1) + torch.einsum("trc,trd->tcd", comb.float(),
+                                                                                X.float())
+
+
+def router_sqrtsoftplus(logits: torch.Tensor, bias: torch.Tensor, topk: int, scaling: float):
+    """score = sqrt(softplus(logit)); top-k by score + bias; weights = the
+    chosen scores / (sum + 1e-20) x scaling."""
+    s = F.softplus(logits.float()).sqrt()
+    ids = (s + bias.float()).topk(topk, dim=-1).indices
+    w = s.gather(1, ids)
+    w = w / (w.sum(-1, keepdim=True) + 1e-20)
+    return w * scaling, ids.to(torch.int32)
+
+
+def e5_prune(ids: torch.Tensor, w: torch.Tensor, budget: float, max_count: int):
+    """E5 routed-expert prune of one batch (in place semantics, returns new
+    tensors): an expert picked by <= max_count rows is eligible; in each row
+    a pick's run is the sum of the eligible weights before it in (weight,
+    slot) order plus its own; it is a candidate when eligible and run <=
+    budget * the row's mass; an expert whose every pick is a candidate is
+    dropped (id -1, weight 0; kept weights are not renormalised)."""
+    ids = ids.clone()
+    w = w.clone().float()
+    T, K = ids.shape
+    valid = ids >= 0
+    count = {}
+    for e in ids[valid].tolist():
+        count[e] = count.get(e, 0) + 1
+    elig = torch.tensor([[bool(valid[t, k]) and count.get(int(ids[t, k]), 0) <= max_count for k in range(K)]
+                         for t in range(T)], dtype=torch.bool).reshape(T, K)
+    cand = torch.zeros(T, K, dtype=torch.bool)
+    for t in range(T):
+        mass = float(w[t][valid[t]].sum())
+        order = sorted(range(K), key=lambda k: (float(w[t, k]), k))
+        run = 0.0
+        for k in order:
+            if not elig[t, k]:
+                continue
+            run += float(w[t, k])
+            cand[t, k] = run <= budget * mass
+    drop = set()
+    for e in set(ids[valid].tolist()):
+        picks = (ids == e)
+        if bool(cand[picks].all()):
+            drop.add(e)
+    for t in range(T):
+        for k in range(K):
+            if int(ids[t, k]) in drop:
+                ids[t, k] = -1
+                w[t, k] = 0.0
+    return w, ids
+
+
+def mqa_sink_attention(q: torch.Tensor, kv_cache: torch.Tensor, kv_scale: float, block_table: torch.Tensor,
+                       q_seq: torch.Tensor, q_pos: torch.Tensor, softmax_scale: float, page_size: int,
+                       sink: Optional[torch.Tensor], L: int,
+                       topk_idx: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """MQA over the paged latent rows: K = V = cache[:, :L]; q [T, H, L];
+    sink [H] (natural-log logits joining each head's softmax denominator)."""
+    T, H, _ = q.shape
+    out = torch.zeros(T, H, L, dtype=torch.float32, device=q.device)
+    kvf = kv_cache.float() * kv_scale
+    for t in range(T):
+        b = int(q_seq[t])
+        n = int(q_pos[t]) + 1
+        pos = torch.arange(n, device=q.device)
+        if topk_idx is not None:
+            sel = topk_idx[t]
+            pos = sel[(sel >= 0) & (sel < n)].long()
+        pages = block_table[b, (pos // page_size).long()].long()
+        k = kvf[pages * page_size + pos % page_size][:, :L]
+        s = (q[t].float() @ k.T) * softmax_scale                       # [H, n]
+        if sink is not None:
+            s = torch.cat([s, sink.float().unsqueeze(-1)], -1)
+            p = s.softmax(-1)[:, :-1]
+        else:
+            p = s.softmax(-1)
+        out[t] = p @ k
+    return out
+
+
+ENGRAM_SALT = 0x9E3779B97F4A7C15
+
+
+def _splitmix64(x: int) -> int:
+    m = (1 << 64) - 1
+    x = (x + ENGRAM_SALT) & m
+    x = ((x ^ (x >> 30)) * 0xBF58476D1CE4E5B9) & m
+    x = ((x ^ (x >> 27)) * 0x94D049BB133111EB) & m
+    return x ^ (x >> 31)
+
+
+def engram_multipliers(heads: int):
+    """Odd 64-bit hash multipliers, one per head (shared by the CUDA kernel)."""
+    return [_splitmix64(j + 1) | 1 for j in range(heads)]
+
+
+def engram_hash(ctx: torch.Tensor, heads: int, rows: int, max_ngram: int) -> torch.Tensor:
+    """ctx [T, max_ngram] int64: token at position p - i in column i (-1
+    where p - i < 0).  Head j hashes an n-gram of order 2 + j % (max_ngram - 1)
+    into its own range of rows // heads rows: h = ((h ^ (tok + 1)) * M_j)
+    over the n-gram (64-bit wrap), row = j * per + (h >> 32) % per."""
+    per = rows // heads
+    mults = engram_multipliers(heads)
+    T = ctx.shape[0]
+    out = torch.empty(T, heads, dtype=torch.int32)
+    span = max(1, max_ngram - 1)
+    for j in range(heads):
+        n = 2 + j % span if max_ngram >= 2 else 1
+        h = torch.zeros(T, dtype=torch.int64)
+        m = mults[j]
+        m_signed = m - (1 << 64) if m >= (1 << 63) else m
+        for i in range(n):
+            v = (ctx[:, i] + 1).clamp(min=0)
+            h = (h ^ v) * m_signed                                      # wrapping int64 == uint64 bits
+        hi = (h >> 32) & 0xFFFFFFFF
+        out[:, j] = (j * per + hi % per).to(torch.int32)
+    return out
+
+
+def e8m0_to_float(e: torch.Tensor) -> torch.Tensor:
+    e = e.to(torch.int32)
+    return torch.where(e == 0, torch.full_like(e, 0, dtype=torch.float32) + 2.0 ** -127,
+                       torch.pow(2.0, (e - 127).float()))
+
+
+def engram_gather(table: torch.Tensor, scale: torch.Tensor, ids: torch.Tensor, row_lo: int = 0,
+                  row_hi: Optional[int] = None) -> torch.Tensor:
+    """table [rows, dim] e4m3 bytes (uint8), scale [rows, dim/32] UE8M0 bytes,
+    ids [T, heads] global row ids -> [T, heads, dim] fp32; rows outside
+    [row_lo, row_hi) of this shard give zeros."""
+    row_hi = row_lo + table.shape[0] if row_hi is None else row_hi
+    T, nh = ids.shape
+    dim = table.shape[1]
+    flat = ids.reshape(-1).long()
+    own = (flat >= row_lo) & (flat < row_hi)
+    loc = (flat - row_lo).clamp(0, table.shape[0] - 1)
+    v = table[loc].view(torch.float8_e4m3fn).float()
+    s = e8m0_to_float(scale[loc]).repeat_interleave(32, -1)
+    out = (v * s) * own.unsqueeze(-1).float()
+    return out.view(T, nh, dim)
+
+
+def engram_gate(X: torch.Tensor, kv: torch.Tensor, q_w: torch.Tensor, k_w: torch.Tensor, eps: float,
+                clamp: float) -> torch.Tensor:
+    """X [T, hc, D]; kv [T, 2D] = [k | v].  Each stream c: a = sigmoid(clamp(
+    <rmsnorm(X_c) * q_w, rmsnorm(k) * k_w> / sqrt(D))), X_c + a * v."""
+    D = X.shape[-1]
+    k, v = kv[:, :D].float(), kv[:, D:].float()
+    kn = rmsnorm(k, k_w, eps)
+    qn = rmsnorm(X.float(), q_w, eps)
+    a = torch.sigmoid(((qn * kn.unsqueeze(1)).sum(-1) / (D ** 0.5)).clamp(-clamp, clamp))
+    return X.float() + a.unsqueeze(-1) * v.unsqueeze(1)
+
+
+def inv_rope_tail(o: torch.Tensor, pos: torch.Tensor, table: torch.Tensor, rd: int) -> torch.Tensor:
+    """Rotate the last rd dims of o [T, H, L] back by each token's position."""
+    cs = table[pos.long()].float()
+    neg = torch.cat([cs[:, : rd // 2], -cs[:, rd // 2:]], -1)
+    tail = rope(o[..., -rd:], torch.arange(o.shape[0]), neg)
+    return torch.cat([o[..., :-rd].float(), tail], -1)

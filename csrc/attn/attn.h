@@ -28,6 +28,7 @@ struct MlaTcArgs {
   const int* topk = nullptr;  // [T, topk_n] cache positions (-1 = none): sparse MLA
   int topk_n = 0;
   int hb = 0;                 // heads per CTA (16 / 32 / 64); 0 = largest that divides H
+  float* lse_out = nullptr;   // [T, H] log-sum-exp (log2 of the sum of 2^(scaled score)), optional
 };
 // Lightning indexer (sparse MLA): key store, query quantisation, tcgen05
 // scores and the top-k radix select.

@@ -58,7 +58,8 @@ void mla_q_prep(const at::Tensor& q_abs, const at::Tensor& q_pe, const at::Tenso
 void mla_tc(const at::Tensor& q8, const at::Tensor& qs, const at::Tensor& cache, double kv_scale,
             const at::Tensor& block_table, const at::Tensor& q_seq, const at::Tensor& q_pos, int64_t page_size,
             double sm_scale, int64_t nsplit, at::Tensor out, c10::optional<at::Tensor> part_o,
-            c10::optional<at::Tensor> part_lse, c10::optional<at::Tensor> topk, int64_t hb) {
+            c10::optional<at::Tensor> part_lse, c10::optional<at::Tensor> topk, int64_t hb,
+            c10::optional<at::Tensor> lse_out) {
   TORCH_CHECK(q8.is_cuda() && q8.dim() == 3 && q8.size(2) == 576 && q8.is_contiguous(), "q8 e4m3 [T,H,576]");
   TORCH_CHECK(cache.dim() == 2 && cache.size(1) == 576 && cache.is_contiguous(), "cache [slots, 576]");
   TORCH_CHECK(block_table.scalar_type() == at::kInt && q_seq.scalar_type() == at::kInt && q_pos.scalar_type() == at::kInt,
@@ -78,6 +79,10 @@ void mla_tc(const at::Tensor& q8, const at::Tensor& qs, const at::Tensor& cache,
   a.page_size = page_size;
   a.nsplit = nsplit;
   a.hb = hb;
+  if (lse_out.has_value() && lse_out->defined()) {
+    TORCH_CHECK(lse_out->scalar_type() == at::kFloat && lse_out->numel() >= (int64_t)a.T * a.H, "lse_out fp32 [T, H]");
+    a.lse_out = reinterpret_cast<float*>(lse_out->data_ptr());
+  }
   a.sm_scale = sm_scale;
   a.kv_scale = kv_scale;
   a.out = out.data_ptr();
@@ -159,7 +164,8 @@ void register_attn(pybind11::module& m) {
   m.def("mla_tc", &mla_tc, pybind11::arg("q8"), pybind11::arg("qs"), pybind11::arg("cache"), pybind11::arg("kv_scale"),
         pybind11::arg("block_table"), pybind11::arg("q_seq"), pybind11::arg("q_pos"), pybind11::arg("page_size"),
         pybind11::arg("sm_scale"), pybind11::arg("nsplit"), pybind11::arg("out"), pybind11::arg("part_o"),
-        pybind11::arg("part_lse"), pybind11::arg("topk") = pybind11::none(), pybind11::arg("hb") = 0);
+        pybind11::arg("part_lse"), pybind11::arg("topk") = pybind11::none(), pybind11::arg("hb") = 0,
+        pybind11::arg("lse_out") = pybind11::none());
   m.def("ix_k_store", &ix_k_store);
   m.def("ix_q_quant", &ix_q_quant);
   m.def("ix_score", &ix_score);

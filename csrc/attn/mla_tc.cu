@@ -94,6 +94,7 @@ struct Params {
   __nv_bfloat16* out;        // [T, H, 512] when nsplit == 1
   float* part_o;             // [nsplit, T, H, 512] when nsplit > 1
   float* part_lse;           // [nsplit, T, H]
+  float* lse_out;            // [T, H] log2-domain log-sum-exp of the scaled scores (optional)
   uint32_t* err;
   const uint8_t* cache;      // e4m3 [rows, 576] (sparse gathers)
   const int* topk;           // [T, topk_n] cache positions, -1 = none (sparse)
@@ -415,14 +416,16 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
           }
         }
       }
-      if (p.nsplit > 1 && tid < HB) {
+      if (tid < HB && (p.nsplit > 1 || p.lse_out)) {
         const float l = sHead[2 * HB + tid];
-        p.part_lse[(int64_t)split * gridDim.x * p.H + (int64_t)t * p.H + h0 + tid] =
-            l > 0.f ? sHead[HB + tid] + log2f(l) : -INFINITY;
+        const float v = l > 0.f ? sHead[HB + tid] + log2f(l) : -INFINITY;
+        if (p.nsplit > 1) p.part_lse[(int64_t)split * gridDim.x * p.H + (int64_t)t * p.H + h0 + tid] = v;
+        else p.lse_out[(int64_t)t * p.H + h0 + tid] = v;
       }
-    } else if (p.nsplit > 1 && tid < HB) {
+    } else if (tid < HB && (p.nsplit > 1 || p.lse_out)) {
       // empty split
-      p.part_lse[(int64_t)split * gridDim.x * p.H + (int64_t)t * p.H + h0 + tid] = -INFINITY;
+      if (p.nsplit > 1) p.part_lse[(int64_t)split * gridDim.x * p.H + (int64_t)t * p.H + h0 + tid] = -INFINITY;
+      else p.lse_out[(int64_t)t * p.H + h0 + tid] = -INFINITY;
     }
     if (nt == 0 && p.nsplit == 1) {
       for (int e = tid; e < HB * kL; e += kSmThreads)
@@ -438,7 +441,8 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
 }
 
 // Merge split partials: out = sum_s 2^(lse_s - M) o_s / sum_s 2^(lse_s - M).
-__global__ void mla_merge_kernel(const float* part_o, const float* part_lse, int nsplit, int TH, __nv_bfloat16* out) {
+__global__ void mla_merge_kernel(const float* part_o, const float* part_lse, int nsplit, int TH, __nv_bfloat16* out,
+                                 float* lse_out) {
   const int th = blockIdx.x;
   pdl_wait();
   pdl_launch_dependents();   // dependents wait for this grid before touching its outputs
@@ -452,6 +456,7 @@ __global__ void mla_merge_kernel(const float* part_o, const float* part_lse, int
     den += w[s];
   }
   const float inv = den > 0.f ? 1.f / den : 0.f;
+  if (lse_out && threadIdx.x == 0) lse_out[th] = den > 0.f ? M + log2f(den) : -INFINITY;
   for (int d = threadIdx.x; d < kL; d += blockDim.x) {
     float acc = 0.f;
     for (int s = 0; s < nsplit && s < 16; ++s)
@@ -577,6 +582,7 @@ static int launch(const MlaTcArgs& a, cudaStream_t st) {
   p.out = reinterpret_cast<__nv_bfloat16*>(a.out);
   p.part_o = a.part_o;
   p.part_lse = a.part_lse;
+  p.lse_out = a.lse_out;
   p.err = a.err;
   p.cache = a.cache;
   p.topk = a.topk;
@@ -588,7 +594,7 @@ static int launch(const MlaTcArgs& a, cudaStream_t st) {
   if (cudaGetLastError() != cudaSuccess) return 1;
   if (a.nsplit > 1) {
     b200::launch_pdl(mla_merge_kernel, dim3(a.T * a.H), dim3(128), 0, st, a.part_o, a.part_lse, a.nsplit, a.T * a.H,
-                                                 reinterpret_cast<__nv_bfloat16*>(a.out));
+                                                 reinterpret_cast<__nv_bfloat16*>(a.out), a.lse_out);
     if (cudaGetLastError() != cudaSuccess) return 2;
   }
   return 0;

@@ -212,12 +212,12 @@ void kv_store(const at::Tensor& kv, const at::Tensor& w, double eps, const at::T
 }
 
 void router(const at::Tensor& logits, const at::Tensor& bias, int64_t G, int64_t topk_group, int64_t K, double scaling,
-            bool renorm, at::Tensor w_out, at::Tensor id_out) {
+            bool renorm, at::Tensor w_out, at::Tensor id_out, int64_t scoring) {
   check_cuda(logits, "logits");
   const c10::cuda::CUDAGuard g(logits.device());
   TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.is_contiguous(), "logits fp32 contiguous");
   check(b200_router(ptr<float>(logits), ptr<float>(bias), logits.size(0), logits.size(1), G, topk_group, K, float(scaling),
-                    renorm ? 1 : 0, ptr<float>(w_out), ptr<int>(id_out), cur_stream()),
+                    renorm ? 1 : 0, int(scoring), ptr<float>(w_out), ptr<int>(id_out), cur_stream()),
         "router");
 }
 
@@ -429,6 +429,7 @@ std::vector<int64_t> graph_kernel_count(int64_t raw_graph) {
 
 void register_attn(pybind11::module& m);
 void register_comm(pybind11::module& m);
+void register_v4(pybind11::module& m);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "b200ds native sm_100a kernels";
@@ -443,7 +444,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_push", &gemm_push);
   m.def("rope", &rope);
   m.def("kv_store", &kv_store);
-  m.def("router", &router);
+  m.def("router", &router, pybind11::arg("logits"), pybind11::arg("bias"), pybind11::arg("G"),
+        pybind11::arg("topk_group"), pybind11::arg("K"), pybind11::arg("scaling"), pybind11::arg("renorm"),
+        pybind11::arg("w_out"), pybind11::arg("id_out"), pybind11::arg("scoring") = 0);
   m.def("moe_align", &moe_align);
   m.def("moe_gather", &moe_gather);
   m.def("moe_combine", &moe_combine);
@@ -467,5 +470,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("graph_kernel_count", &graph_kernel_count);
   m.def("fill_bytes", &fill_bytes);
   register_attn(m);
+  register_v4(m);
   register_comm(m);
 }

@@ -11,8 +11,9 @@ int b200_rope(void* x, int f32, int64_t st_t, int64_t st_h, int T, int H, int d,
               cudaStream_t st);
 int b200_kv_store(const void* kv, int f32, int64_t ld, int T, int L, int R, const float* w, float eps, const int* pos,
                   const float* table, const int64_t* slots, uint8_t* cache, float kv_scale, cudaStream_t st);
+// scoring 0: sigmoid (DeepSeek-V3); 1: sqrt(softplus) (DeepSeek-V4 family).
 int b200_router(const float* logits, const float* bias, int T, int E, int G, int topk_group, int K, float scaling,
-                int renorm, float* w_out, int* id_out, cudaStream_t st);
+                int renorm, int scoring, float* w_out, int* id_out, cudaStream_t st);
 int b200_moe_align(const int* ids, const float* w, int T, int K, int first, int E, int* seg_start, int* seg_count,
                    int* row_token, float* row_weight, int* pair_row, int* total_rows, int bn1, int* ttile1, int bn2,
                    int* ttile2, cudaStream_t st);
@@ -43,3 +44,28 @@ int b200_sample_final(const void* cand, int B, int Kc, int world, const ArPeers*
 // row r at x[r * ldx + (k / seg) * seg_stride + k % seg].
 int b200_quant_mxfp8_seg(const void* x, int x_is_f32, int ldx, int rows, int K, int seg, int64_t seg_stride,
                          uint8_t* q, uint8_t* sf, cudaStream_t st);
+
+// DeepSeek-V4 family (see v4.cu): mHC stream mixing, Engram, MQA prep, E5.
+int b200_hc_post(void* X, const void* y, int64_t ldy, const float* post, const float* comb, int T, int hc, int D,
+                 float* sumsq, cudaStream_t st);
+int b200_hc_pre(const float* raw, int ldr, int parts, int pstride, const float* sumsq, const float* scale,
+                const float* base, int mode, int iters, float eps, float inv_width, const void* X, int T, int hc,
+                int D, const float* norm_w, float norm_eps, float* post, float* comb, uint8_t* q, uint8_t* sf,
+                void* hb, float* hf, cudaStream_t st);
+int b200_hc_mean(const void* X, int T, int hc, int D, void* out, cudaStream_t st);
+int b200_engram_hash(const int* ids, const int* pos, const int* q_seq, const int* block_table, int bt_stride,
+                     const int64_t* out_slots, int page_size, int* tok_cache, int T, int heads, int per_head,
+                     int max_n, const unsigned long long* mults, int* out, cudaStream_t st);
+int b200_engram_gather(const uint8_t* table, const uint8_t* scale, const int* ids, int n, int row_lo, int row_hi,
+                       void* out, cudaStream_t st);
+int b200_engram_gate(void* X, int T, int hc, int D, const void* kv, int kv_f32, int64_t ldkv, const float* q_w,
+                     const float* k_w, float eps, float clampv, float* sumsq, cudaStream_t st);
+int b200_hc_embed(const void* embed, const int* ids, int T, int hc, int D, void* X, float* sumsq, cudaStream_t st);
+int b200_kv_store_v4(const void* kv, int f32, int64_t ld, int T, int L, int rd, const float* w, float eps,
+                     const int* pos, const float* table, const int64_t* slots, uint8_t* cache, float kv_scale,
+                     cudaStream_t st);
+int b200_mqa_q_prep(const void* q, int64_t qt, int64_t qh, int T, int H, int rd, const int* pos, const float* table,
+                    uint8_t* q8, float* qs, cudaStream_t st);
+int b200_attn_fixup(void* o, int T, int H, const float* lse, const float* sink, int rd, const int* pos,
+                    const float* table, cudaStream_t st);
+int b200_e5_prune(int* ids, float* w, int T, int K, int E, float budget, int max_count, cudaStream_t st);

@@ -82,10 +82,10 @@ __global__ void kv_store_kernel(const void* kv, int f32, int64_t ld, int T, int 
 // top-2 choices in each of G groups; keep the top `topk_group` groups; pick
 // the top-k choices among them; weights = scores renormalised * scaling.
 // Ties resolve to the lower expert index.
-constexpr int kMaxEPerLane = 8;
+constexpr int kMaxEPerLane = 16;   // up to 512 experts
 
 __global__ void router_kernel(const float* logits, const float* bias, int T, int E, int G, int topk_group, int K,
-                              float scaling, int renorm, float* w_out, int* id_out) {
+                              float scaling, int renorm, int scoring, float* w_out, int* id_out) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   pdl_wait();
@@ -98,7 +98,8 @@ __global__ void router_kernel(const float* logits, const float* bias, int T, int
     if (i < per) {
       const int e = lane * per + i;
       const float l = logits[(int64_t)warp * E + e];
-      sc[i] = 1.0f / (1.0f + __expf(-l));
+      // sigmoid (V3) or sqrt(softplus) (V4; softplus(l) = l above 20)
+      sc[i] = scoring == 0 ? 1.0f / (1.0f + __expf(-l)) : sqrtf(l > 20.f ? l : log1pf(expf(l)));
       ch[i] = sc[i] + bias[e];
     } else {
       sc[i] = 0.f;
@@ -252,12 +253,12 @@ int b200_kv_store(const void* kv, int f32, int64_t ld, int T, int L, int R, cons
 }
 
 int b200_router(const float* logits, const float* bias, int T, int E, int G, int topk_group, int K, float scaling,
-                int renorm, float* w_out, int* id_out, cudaStream_t st) {
+                int renorm, int scoring, float* w_out, int* id_out, cudaStream_t st) {
   if (T <= 0) return 0;
   if (E % 32 != 0 || E / 32 > kMaxEPerLane || K > 32 || (G > 1 && (32 % G != 0))) return -1;
   const int threads = 128;
   b200::launch_pdl(router_kernel, dim3((T * 32 + threads - 1) / threads), dim3(threads), 0, st, logits, bias, T, E, G, topk_group, K, scaling,
-                                                                       renorm, w_out, id_out);
+                                                                       renorm, scoring, w_out, id_out);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
 

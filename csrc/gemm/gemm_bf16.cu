@@ -14,8 +14,10 @@
 //                rope part, takes the amax over the 576 values and writes the
 //                e4m3 query + fp32 scale the MLA kernel consumes;
 //   kMxfp8Rows   absorb_o fused with the output projection's MXFP8 quant:
-//                head b's 128 rows are columns [128 b, 128 b + 128) of the
-//                o_proj operand row; a warp's 32 lanes are one UE8M0 block.
+//                batch b's M rows are columns [M b, M b + M) of the output
+//                projection's operand row (V3: value absorption per head,
+//                M = 128; V4: grouped low-rank wo_a per head group, M = rank);
+//                a warp's 32 lanes are one UE8M0 block.
 //
 // Warp roles: warp 0 TMA producer, warp 1 TMEM owner + MMA issuer, warps 2-5
 // epilogue.  All waits are bounded.
@@ -219,13 +221,13 @@ bf16_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
             }
           }
       } else if constexpr (EPI == kMxfp8Rows) {
-        const int kb = p.B * kTileM / 32;
+        const int kb = p.B * p.M / 32;
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 16) {
           uint32_t r[16];
           tmem_ld_x16(lane_addr + c0, r);
           tmem_ld_wait();
-          const int col = b * kTileM + rl;         // o_proj operand column
+          const int col = b * p.M + m0 * kTileM + rl;   // output-projection operand column
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const float v = __uint_as_float(r[j]);
@@ -235,7 +237,7 @@ bf16_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
             const int ex = ceil_log2_bits(amax * (1.0f / 448.0f));
             const int t = t0 + c0 + j;
             if (t < p.T) {
-              p.q[(int64_t)t * p.B * kTileM + col] = uint8_t(f2_to_e4m3x2(v * exp2_int(-ex), 0.f) & 0xFF);
+              p.q[(int64_t)t * p.B * p.M + col] = uint8_t(f2_to_e4m3x2(v * exp2_int(-ex), 0.f) & 0xFF);
               if (lane == 0) p.sf[sf_offset(t, col >> 5, kb)] = uint8_t(ex + 127);
             }
           }
@@ -378,7 +380,6 @@ int b200_bf16_gemm(const Bf16GemmArgs* a, cudaStream_t st) {
       p.ob = a->out_bs;
       return launch_bn<kF32Atomic, 1>(*a, p, st);
     case kMxfp8Rows:
-      if (a->M != 128) return -1;
       p.q = a->q;
       p.sf = a->sf;
       return launch_bn<kMxfp8Rows, 1>(*a, p, st);

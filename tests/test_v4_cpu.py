@@ -1,0 +1,134 @@
+"""DeepSeek-V4 family on CPU: mHC coefficient properties, the E5 prune rule,
+Engram hashing through the per-slot token cache, the engine's V4 model
+against the fp32 oracle (greedy tokens, logits), and TP=2 over gloo."""
+import torch
+
+from mp_util import run_ranks
+
+
+def test_sinkhorn_doubly_stochastic_and_coeff_ranges():
+    from b200ds.ops import ref
+    g = torch.Generator().manual_seed(0)
+    raw = torch.randn(6, 24, generator=g)
+    ss = torch.rand(6, generator=g) * 1024 + 512          # rms ~ 1
+    pre, post, comb = ref.hc_coeffs(raw, ss, torch.ones(3), torch.zeros(24), 4, 1024, 20, 1e-6)
+    # ends on a column pass: columns exact, rows converged
+    assert torch.allclose(comb.sum(-1), torch.ones(6, 4), atol=1e-3)
+    assert torch.allclose(comb.sum(-2), torch.ones(6, 4), atol=1e-5)
+    assert (pre > 0).all() and (pre <= 1 + 1e-5).all() and (post >= 0).all() and (post <= 2).all()
+
+
+def test_e5_prune_rule():
+    from b200ds.ops import ref
+    # rows: (0: heavy 5 / light 7), (1: heavy 5 / light 6 shared with row 2), (2: 6 light / 4 heavy)
+    ids = torch.tensor([[5, 7], [5, 6], [4, 6]], dtype=torch.int32)
+    w = torch.tensor([[0.8, 0.2], [0.7, 0.3], [0.9, 0.1]])
+    w2, ids2 = ref.e5_prune(ids, w, budget=0.4, max_count=1)
+    # 7: picked once, its run 0.2 <= 0.4 -> dropped; 6: picked twice -> not eligible at max_count 1
+    assert ids2.tolist() == [[5, -1], [5, 6], [4, 6]] and float(w2[0, 1]) == 0.0
+    w3, ids3 = ref.e5_prune(ids, w, budget=0.4, max_count=2)
+    # max_count 2: 6 is eligible in both rows and each pick is within budget -> dropped
+    assert ids3.tolist() == [[5, -1], [5, -1], [4, -1]]
+    # weights of kept picks are not renormalised
+    assert float(w3[0, 0]) == float(w[0, 0])
+
+
+def test_engram_hash_matches_full_context():
+    """Hash ids computed chunk by chunk through the per-slot token cache
+    equal the ids from the whole sequence."""
+    from b200ds import ops
+    from b200ds.config import tiny_v4_config
+    from b200ds.models.batch import build_batch
+    from b200ds.models.reference_v4 import engram_context
+    from b200ds.ops import ref
+    cfg = tiny_v4_config()
+    toks = list(range(3, 40, 2))
+    page = 8
+    pages = [5, 2, 9]
+    tok_cache = torch.full((16 * page,), -1, dtype=torch.int32)
+    mults = torch.tensor([v - (1 << 64) if v >= (1 << 63) else v for v in ref.engram_multipliers(cfg.engram_heads)])
+    got = []
+    for st, en in ((0, 7), (7, 12), (12, 13), (13, len(toks))):
+        fb = build_batch([{"tokens": toks[st:en], "start": st, "pages": pages}], page)
+        got.append(ops.engram_ids(fb, tok_cache, cfg, mults, page))
+    want = ref.engram_hash(engram_context(torch.tensor(toks), cfg.engram_max_ngram), cfg.engram_heads,
+                           cfg.engram_rows, cfg.engram_max_ngram)
+    assert torch.equal(torch.cat(got), want)
+
+
+def _v4_engine(prefix_cache=False, chunk=64, tp=1, ps=None):
+    from b200ds import build_model_from
+    from b200ds.config import EngineConfig, tiny_v4_config
+    from b200ds.engine.engine import Engine
+    from b200ds.models.reference_v4 import init_weights_v4
+    cfg = tiny_v4_config()
+    ecfg = EngineConfig(page_size=8, cuda_graphs=False, enable_prefix_cache=prefix_cache, max_prefill_tokens=chunk,
+                        tp_size=tp, ep_size=tp)
+    kw = {"ps": ps} if ps is not None else {}
+    return Engine(build_model_from(cfg, ecfg, init_weights_v4(cfg, 0), device="cpu", **kw), ecfg), cfg
+
+
+def _prompts(cfg, n=3, s=11, seed=1):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(0, cfg.vocab_size, (n, s), generator=g)
+
+
+def test_v4_engine_matches_oracle_greedy():
+    """Paged MQA + sinks + inverse rope + grouped wo_a, mHC kernels' CPU
+    references, sqrt-softplus routing with the E5 prune at decode, Engram
+    through the token cache under chunked prefill: same greedy tokens and
+    close logits as the fp32 oracle."""
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.reference_v4 import ReferenceV4Model, init_weights_v4
+    eng, cfg = _v4_engine(chunk=7)
+    prompts = _prompts(cfg)
+    outs = eng.generate(prompts.tolist(), SamplingParams(max_tokens=6))
+    oracle = ReferenceV4Model(cfg, init_weights_v4(cfg, 0), 256)
+    assert [o.token_ids for o in outs] == oracle.greedy(prompts, 6).tolist()
+
+
+def test_v4_prefill_logits_match_oracle():
+    from b200ds.models.batch import build_batch
+    from b200ds.models.reference_v4 import ReferenceV4Model, init_weights_v4
+    eng, cfg = _v4_engine()
+    prompts = _prompts(cfg, 2, 13, seed=5)
+    seqs = [{"tokens": prompts[b].tolist(), "start": 0, "pages": eng.pool.alloc(2)} for b in range(2)]
+    logits = eng.model.forward(build_batch(seqs, 8))
+    oracle = ReferenceV4Model(cfg, init_weights_v4(cfg, 0), 64)
+    oracle.reset(2)
+    want = oracle.forward(prompts, 0, decode=False)[:, -1]
+    assert torch.allclose(logits, want, rtol=1e-4, atol=1e-4), (logits - want).abs().max()
+    assert len(eng.model.aux) == len(cfg.aux_layers) and eng.model.aux[0].shape == (26, cfg.hidden_size)
+
+
+def test_v4_prefix_cache_transparent():
+    from b200ds.engine.request import SamplingParams
+    eng, cfg = _v4_engine(prefix_cache=True)
+    g = torch.Generator().manual_seed(4)
+    shared = torch.randint(0, cfg.vocab_size, (24,), generator=g).tolist()
+    p1, p2 = shared + [5, 6, 7], shared + [8, 9]
+    first = eng.generate([p1], SamplingParams(max_tokens=5))[0].token_ids
+    again = eng.generate([p2], SamplingParams(max_tokens=5))[0].token_ids
+    ref_eng, _ = _v4_engine(prefix_cache=False)
+    assert ref_eng.generate([p1], SamplingParams(max_tokens=5))[0].token_ids == first
+    assert ref_eng.generate([p2], SamplingParams(max_tokens=5))[0].token_ids == again
+
+
+def _tp_rank(rank, world):
+    from b200ds.engine.request import SamplingParams
+    from b200ds.parallel.state import init_parallel
+    ps = init_parallel(backend="gloo")
+    eng, cfg = _v4_engine(tp=world, ps=ps)
+    outs = eng.generate(_prompts(cfg).tolist(), SamplingParams(max_tokens=6))
+    return [o.token_ids for o in outs]
+
+
+def test_v4_tp2_gloo_matches_single():
+    """Heads / output groups / FFN columns split, experts EP-split, Engram
+    table rows sharded (zero rows summed by the all-reduce), vocab-parallel
+    head: both ranks produce the single-process tokens."""
+    from b200ds.engine.request import SamplingParams
+    res = run_ranks(_tp_rank, 2)
+    eng, cfg = _v4_engine()
+    single = [o.token_ids for o in eng.generate(_prompts(cfg).tolist(), SamplingParams(max_tokens=6))]
+    assert res[0] == single and res[1] == single
