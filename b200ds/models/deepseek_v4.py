@@ -207,6 +207,14 @@ class DeepseekV4Model:
 # construction from a full state dict (names of models/reference_v4.py)
 # ---------------------------------------------------------------------------
 
+def host_mapped_copy(t: torch.Tensor) -> torch.Tensor:
+    """Copy of a CPU tensor in device-mapped host memory."""
+    from .. import _C
+    buf = _C.host_mapped(t.numel() * t.element_size()).view(t.dtype).view(t.shape)
+    buf.copy_(t)
+    return buf
+
+
 def build_model_v4(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState, sd: Dict[str, torch.Tensor],
                    device="cpu", kv_dtype=None) -> DeepseekV4Model:
     """This rank's V4 model from a FULL (unsharded) fp32 state dict:
@@ -238,8 +246,12 @@ def build_model_v4(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState, sd: 
         return t.chunk(n, dim)[r].contiguous() if n > 1 else t
 
     def hcw(prefix) -> HcWeights:
-        return HcWeights(get(prefix + "fn").to(dev).contiguous(), get(prefix + "scale").to(dev),
-                         get(prefix + "base").to(dev))
+        w = HcWeights(get(prefix + "fn").to(dev).contiguous(), get(prefix + "scale").to(dev),
+                      get(prefix + "base").to(dev))
+        if dev.type == "cuda":
+            from ..ops.cuda import hc_fn_parts
+            w.fn_parts = hc_fn_parts(w.fn)
+        return w
 
     layers: List[V4LayerWeights] = []
     for i in range(cfg.num_hidden_layers):
@@ -261,8 +273,9 @@ def build_model_v4(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState, sd: 
             lo, hi = tr * rows // tp, (tr + 1) * rows // tp
             t_sh, s_sh = table[lo:hi].contiguous(), scale[lo:hi].contiguous()
             if dev.type == "cuda":
-                # host-resident tables, read by the gather kernel through their device mapping
-                t_sh, s_sh = t_sh.pin_memory(), s_sh.pin_memory()
+                # host-resident tables (mapped host memory), read by the gather
+                # kernel over the host link
+                t_sh, s_sh = host_mapped_copy(t_sh), host_mapped_copy(s_sh)
             eng = EngramWeights(table=t_sh, scale=s_sh, row_lo=lo,
                                 wkv=Linear(_quantize(get(e + "wkv.weight"), fmt_d, dev)),
                                 q_w=get(e + "q_norm.weight").to(dev), k_w=get(e + "k_norm.weight").to(dev))

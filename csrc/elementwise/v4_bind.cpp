@@ -63,13 +63,23 @@ void engram_hash(const at::Tensor& ids, const at::Tensor& pos, const at::Tensor&
       "engram_hash");
 }
 
-// table / scale: device tensors or pinned host tensors (read through their
+// Host memory mapped into the device address space (cudaHostAllocMapped):
+// the Engram tables live here and the gather kernel reads them directly.
+at::Tensor host_mapped(int64_t nbytes) {
+  void* p = nullptr;
+  TORCH_CHECK(cudaHostAlloc(&p, nbytes > 0 ? nbytes : 1, cudaHostAllocMapped | cudaHostAllocPortable) == cudaSuccess,
+              "cudaHostAlloc failed");
+  return torch::from_blob(p, {nbytes}, [](void* q) { cudaFreeHost(q); },
+                          at::TensorOptions().dtype(at::kByte).device(at::kCPU));
+}
+
+// table / scale: device tensors or host_mapped tensors (read through their
 // device mapping)
 const uint8_t* device_view(const at::Tensor& t) {
   if (t.is_cuda()) return reinterpret_cast<const uint8_t*>(t.data_ptr());
-  TORCH_CHECK(t.is_pinned(), "host Engram tables must be pinned");
   void* d = nullptr;
-  TORCH_CHECK(cudaHostGetDevicePointer(&d, t.data_ptr(), 0) == cudaSuccess, "host table not mapped");
+  TORCH_CHECK(cudaHostGetDevicePointer(&d, t.data_ptr(), 0) == cudaSuccess,
+              "host Engram tables must come from host_mapped()");
   return reinterpret_cast<const uint8_t*>(d);
 }
 
@@ -152,6 +162,7 @@ void register_v4(pybind11::module& m) {
   m.def("hc_embed", &hc_embed);
   m.def("engram_hash", &engram_hash);
   m.def("engram_gather", &engram_gather);
+  m.def("host_mapped", &host_mapped);
   m.def("engram_gate", &engram_gate);
   m.def("kv_store_v4", &kv_store_v4);
   m.def("mqa_q_prep", &mqa_q_prep);

@@ -1,0 +1,208 @@
+"""DeepSeek-V4-family kernels on the GPU against the fp32 references in
+b200ds.ops.ref, and the small V4 model end to end against the fp32 oracle."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+@pytest.fixture(autouse=True)
+def _native():
+    from b200ds import ops
+    ops.set_impl("native")
+    import b200ds._C  # noqa: F401  (loud failure if the extension is missing)
+
+
+def rel_err(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / (b.norm() + 1e-12)).item()
+
+
+def _streams(T, D, seed=0):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    return torch.randn(T, 4, D, device=DEV, generator=g).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("T,D", [(3, 1024), (37, 5120)])
+def test_hc_post(T, D):
+    from b200ds.ops import cuda, ref
+    X = _streams(T, D)
+    y = torch.randn(T, D, device=DEV).to(torch.bfloat16)
+    post = torch.rand(T, 4, device=DEV) * 2
+    comb = torch.rand(T, 16, device=DEV)
+    want = ref.hc_post(X.float(), y.float(), post, comb.view(T, 4, 4))
+    ss = cuda.hc_post(X, y, post, comb)
+    assert rel_err(X, want) < 4e-3
+    assert torch.allclose(ss, X.float().pow(2).sum((1, 2)), rtol=1e-4)
+
+
+@pytest.mark.parametrize("T,D,head", [(5, 1024, False), (64, 1024, False), (130, 5120, False), (9, 1024, True)])
+def test_hc_pre_stats_gemm_and_coeffs(T, D, head):
+    """tcgen05 stats GEMM (fn in bf16 hi/mid/lo parts, split-K) + the
+    coefficient / Sinkhorn / combine / RMSNorm / MXFP8 kernel."""
+    from b200ds.ops import HcWeights, cuda, ref
+    from b200ds.ops.quant import dequant_mxfp8
+    from b200ds.config import small_v4_gpu_config
+    cfg = small_v4_gpu_config()
+    X = _streams(T, D, 1)
+    M = 4 if head else 24
+    g = torch.Generator(device=DEV).manual_seed(2)
+    hw = HcWeights(torch.randn(M, 4 * D, device=DEV, generator=g) * 0.02,
+                   torch.ones(1 if head else 3, device=DEV), torch.randn(M, device=DEV, generator=g))
+    w = torch.rand(D, device=DEV) + 0.5
+    ss = X.float().pow(2).sum((1, 2))
+    raw = X.float().flatten(1) @ hw.fn.T
+    if head:
+        pre = ref.hc_head_coeffs(raw, ss, hw.scale, hw.base, 4, 4 * D, cfg.hc_eps)
+    else:
+        pre, post, comb = ref.hc_coeffs(raw, ss, hw.scale, hw.base, 4, 4 * D, cfg.hc_sinkhorn_iters, cfg.hc_eps)
+    h_ref = ref.rmsnorm(ref.hc_combine(X.float(), pre), w, 1e-6)
+
+    class _Q:
+        quantized = True
+    a, p2, c2 = cuda.hc_pre(X, ss, hw, w, 1e-6, cfg, _Q(), head, True)
+    if not head:
+        assert torch.allclose(p2, post, atol=2e-4, rtol=1e-4)
+        assert torch.allclose(c2.view(T, 4, 4), comb, atol=2e-4, rtol=1e-3)
+    assert rel_err(a.hf, h_ref) < 5e-3
+    assert rel_err(dequant_mxfp8(a.q, a.sf), h_ref) < 4e-2
+
+
+def test_hc_embed_and_mean():
+    from b200ds.ops import cuda
+    emb = torch.randn(100, 1024, device=DEV).to(torch.bfloat16)
+    ids = torch.tensor([3, 7, 99, 3], dtype=torch.int32, device=DEV)
+    X, ss = cuda.hc_embed(emb, ids, 4)
+    assert torch.equal(X, emb[ids.long()].unsqueeze(1).expand(-1, 4, -1))
+    assert torch.allclose(ss, 4 * emb[ids.long()].float().pow(2).sum(-1), rtol=1e-4)
+    assert torch.allclose(cuda.hc_mean(X).float(), emb[ids.long()].float(), atol=1e-2)
+
+
+def test_engram_hash_gather_gate():
+    from b200ds import ops
+    from b200ds.config import tiny_v4_config
+    from b200ds.models.batch import build_batch
+    from b200ds.ops import EngramWeights, cuda, ref
+    from b200ds.models.deepseek import Linear
+    cfg = tiny_v4_config(hidden_size=1024, engram_heads=8, engram_rows=4096)
+    mults = torch.tensor([v - (1 << 64) if v >= (1 << 63) else v for v in ref.engram_multipliers(8)])
+    toks = list(range(11, 90, 3))
+    page = 64
+    tc_cpu = torch.full((8 * page,), -1, dtype=torch.int32)
+    tc_gpu = tc_cpu.to(DEV)
+    for st, en in ((0, 9), (9, 10), (10, len(toks))):
+        fb = build_batch([{"tokens": toks[st:en], "start": st, "pages": [3, 1]}], page)
+        want = ops.engram_ids(fb, tc_cpu, cfg, mults, page)
+        got = cuda.engram_ids(fb.to(DEV), tc_gpu, cfg, mults.to(DEV), page)
+        assert torch.equal(got.cpu(), want)
+    # gather from a pinned host shard (rows [1024, 3072) of the table)
+    g = torch.Generator().manual_seed(3)
+    table = (torch.randn(2048, 256, generator=g)).clamp(-448, 448).to(torch.float8_e4m3fn).view(torch.uint8)
+    scale = torch.randint(110, 135, (2048, 8), generator=g, dtype=torch.uint8)
+    ids = torch.randint(0, 4096, (5, 8), generator=g, dtype=torch.int32)
+    want = ref.engram_gather(table, scale, ids, 1024, 3072)
+    out = torch.empty(40, 256, dtype=torch.bfloat16, device=DEV)
+    from b200ds import _C
+    from b200ds.models.deepseek_v4 import host_mapped_copy
+    _C.engram_gather(host_mapped_copy(table), host_mapped_copy(scale), ids.to(DEV), 1024, out)
+    assert torch.equal(out.float().cpu().view(5, 8, 256), want)
+    # gate
+    X = _streams(5, 1024, 4)
+    kv = torch.randn(5, 2048, device=DEV).to(torch.bfloat16)
+    qw, kw = torch.rand(1024, device=DEV) + 0.5, torch.rand(1024, device=DEV) + 0.5
+    want = ref.engram_gate(X.float(), kv.float(), qw, kw, 1e-6, 10.0)
+    ss = torch.empty(5, device=DEV)
+    _C.engram_gate(X, kv, qw, kw, 1e-6, 10.0, ss)
+    assert rel_err(X, want) < 4e-3
+    assert torch.allclose(ss, X.float().pow(2).sum((1, 2)), rtol=1e-4)
+
+
+@pytest.mark.parametrize("T,ctx,sink", [(4, 200, True), (16, 1000, True), (3, 70, False)])
+def test_mqa_sink_attention(T, ctx, sink):
+    """kv_store_v4 (RMSNorm + RoPE tail + e4m3) and the MQA path (query
+    prep, tcgen05 latent attention with LSE, sink + inverse-RoPE fix-up)
+    against the fp32 reference on the same cache."""
+    from types import SimpleNamespace
+    from b200ds import ops
+    from b200ds.config import small_v4_gpu_config
+    from b200ds.models.rope import cos_sin_table
+    cfg = small_v4_gpu_config()
+    H, L, rd, ps = 16, 512, 64, 64
+    table = cos_sin_table(cfg, 4096, device=DEV)
+    pages = (ctx + ps - 1) // ps
+    bt = (torch.arange(T * pages, dtype=torch.int32).view(T, pages) + 1).to(DEV)
+    cache = torch.zeros((T * pages + 1) * ps, 576, dtype=torch.float8_e4m3fn, device=DEV)
+    kv = torch.randn(T * ctx, L, device=DEV).to(torch.bfloat16)
+    pos = torch.arange(ctx, dtype=torch.int32, device=DEV).repeat(T)
+    seq = torch.arange(T, dtype=torch.int32, device=DEV).repeat_interleave(ctx)
+    slots = (bt[seq.long(), (pos // ps).long()].long() * ps + (pos % ps).long())
+    w = torch.rand(L, device=DEV) + 0.5
+    ops.kv_store_v4(kv, w, 1e-6, table, pos, cache, slots, 1.0, rd)
+    cache_ref = torch.zeros(cache.shape, dtype=torch.float32)
+    ops.kv_store_v4(kv.float().cpu(), w.cpu(), 1e-6, table.cpu(), pos.cpu(), cache_ref, slots.cpu(), 1.0, rd)
+    assert rel_err(cache.float().cpu(), cache_ref) < 4e-2
+    q = (torch.randn(T, H, L, device=DEV) * 0.3).to(torch.bfloat16)
+    fb = SimpleNamespace(block_table=bt, q_seq=torch.arange(T, dtype=torch.int32, device=DEV),
+                         positions=torch.full((T,), ctx - 1, dtype=torch.int32, device=DEV), is_decode=True,
+                         max_seq_len=ctx)
+    snk = (torch.randn(H, device=DEV) * 2) if sink else None
+    o = ops.mqa_attention(q, cache, 1.0, fb, cfg.softmax_scale, ps, snk, table, rd)
+    fbc = SimpleNamespace(block_table=bt.cpu(), q_seq=fb.q_seq.cpu(), positions=fb.positions.cpu())
+    want = ops.mqa_attention(q.float().cpu(), cache.float().cpu(), 1.0, fbc, cfg.softmax_scale, ps,
+                             snk.cpu() if sink else None, table.cpu(), rd)
+    assert rel_err(o.cpu(), want) < 3e-2, rel_err(o.cpu(), want)
+
+
+def test_router_sqrtsoftplus_and_e5_prune():
+    from b200ds.config import small_v4_gpu_config
+    from b200ds.ops import cuda, ref
+    cfg = small_v4_gpu_config(n_routed_experts=256)
+    T = 48
+    g = torch.Generator(device=DEV).manual_seed(5)
+    x = torch.randn(T, 1024, device=DEV, generator=g).to(torch.bfloat16)
+    gate = torch.randn(256, 1024, device=DEV, generator=g) * 0.05
+    bias = torch.randn(256, device=DEV, generator=g) * 0.01
+    w, ids = cuda.router(x, gate, bias, cfg)
+    logits = x.float() @ gate.to(torch.bfloat16).float().T
+    w_ref, ids_ref = ref.router_sqrtsoftplus(logits, bias, cfg.num_experts_per_tok, cfg.routed_scaling_factor)
+    same = (ids.sort(-1).values == ids_ref.sort(-1).values).all(-1)
+    assert same.float().mean() > 0.95
+    assert torch.allclose(w.sort(-1).values[same], w_ref.sort(-1).values[same], rtol=1e-3, atol=1e-4)
+    w2, ids2 = cuda.e5_prune(w.clone(), ids.clone(), cfg, 256)
+    w3, ids3 = ref.e5_prune(ids.cpu(), w.cpu(), cfg.prune_budget, cfg.prune_max_count)
+    assert torch.equal(ids2.cpu(), ids3) and torch.allclose(w2.cpu(), w3)
+    assert int((ids3 < 0).sum()) > 0          # the batch does prune something
+
+
+def test_small_v4_model_matches_oracle_and_graphs():
+    """small V4 model (tcgen05 GEMMs, fused experts, mHC / Engram / MQA
+    kernels) vs the fp32 oracle on the same weights; decode through CUDA
+    graphs gives the eager tokens."""
+    from b200ds import build_model_from
+    from b200ds.config import EngineConfig, small_v4_gpu_config
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.batch import build_batch
+    from b200ds.models.reference_v4 import ReferenceV4Model, init_weights_v4
+    cfg = small_v4_gpu_config()
+    sd = init_weights_v4(cfg, 0)
+    ecfg = EngineConfig(page_size=64, max_kv_pages=64, cuda_graphs=False)
+    m = build_model_from(cfg, ecfg, sd, device=DEV)
+    eng = Engine(m, ecfg)
+    g = torch.Generator().manual_seed(0)
+    prompts = torch.randint(0, cfg.vocab_size, (2, 40), generator=g)
+    seqs = [{"tokens": prompts[b].tolist(), "start": 0, "pages": eng.pool.alloc(1)} for b in range(2)]
+    logits = m.forward(build_batch(seqs, 64, device=DEV)).float().cpu()
+    oracle = ReferenceV4Model(cfg, sd, 128)
+    oracle.reset(2)
+    want = oracle.forward(prompts, 0, decode=False)[:, -1]
+    assert rel_err(logits, want) < 0.15, rel_err(logits, want)
+    eager = Engine(build_model_from(cfg, ecfg, sd, device=DEV), ecfg)
+    toks_e = [o.token_ids for o in eager.generate(prompts.tolist(), SamplingParams(max_tokens=8))]
+    ecfg_g = EngineConfig(page_size=64, max_kv_pages=64, cuda_graphs=True, graph_batch_sizes=(2,), max_num_seqs=2)
+    graphs = Engine(build_model_from(cfg, ecfg_g, sd, device=DEV), ecfg_g)
+    toks_g = [o.token_ids for o in graphs.generate(prompts.tolist(), SamplingParams(max_tokens=8))]
+    torch.cuda.synchronize()
+    assert toks_g == toks_e
