@@ -36,6 +36,9 @@ def build_model_from(cfg: ModelConfig, ecfg: EngineConfig, weights: Union[str, d
         if isinstance(weights, dict):
             sd = weights
         elif weights == "random":
+            from .models import random_init
+            if random_init.should_generate_on_device(cfg, device):
+                return random_init.build_random_model_v4(cfg, ecfg, ps, device, seed)
             sd = init_weights_v4(cfg, seed=seed)
         else:
             sd = loader.load_checkpoint(weights)

@@ -181,3 +181,85 @@ def _gate_up(I: int, h: int, dev, sd) -> MXFP8Tensor:
     """[gate; up] stacked rows with I a multiple of 128 per half."""
     assert I % 128 == 0, I
     return rand_mx((), 2 * I, h, dev, sd)
+
+
+def build_random_model_v4(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState, device, seed: int = 0,
+                          reserve_bytes: Optional[float] = None):
+    """DeepSeek-V4-family model with random weights generated on the device
+    in the serving formats (same conventions as above); Engram tables are
+    random e4m3 rows in mapped host memory (this rank's row shard)."""
+    from ..ops import EngramWeights, HcWeights
+    from ..ops.cuda import hc_fn_parts
+    from .deepseek_v4 import DeepseekV4Model, V4AttnWeights, V4LayerWeights, host_mapped_copy
+    dev = torch.device(device)
+    gen = torch.Generator(device=dev).manual_seed(seed + 7919 * ps.rank)
+    sd = _Seeder(seed * 131 + ps.rank)
+    tp, tr = ps.tp_size, ps.tp_rank
+    h, hc = cfg.hidden_size, cfg.hc_mult
+    H, L, G, R = cfg.num_attention_heads, cfg.kv_lora_rank, cfg.o_groups, cfg.o_lora_rank
+    Hl, Gl = H // tp, G // tp
+    ones = lambda n: torch.ones(n, dtype=torch.float32, device=dev)
+
+    def hcw(m: int) -> HcWeights:
+        fn = rand_bf16((m, hc * h), dev, gen, dtype=torch.float32)
+        base = torch.zeros(m, device=dev)
+        if m > hc:
+            base[2 * hc:] = (torch.eye(hc, device=dev) * 4.0).flatten()
+        w = HcWeights(fn, ones(3 if m > hc else 1), base)
+        w.fn_parts = hc_fn_parts(fn)
+        return w
+
+    M = (2 + hc) * hc
+    n_moe = sum(1 for i in range(cfg.num_hidden_layers) if cfg.is_moe_layer(i))
+    per = cfg.n_routed_experts // ps.ep_size
+    first = ps.ep_rank * per
+    I = cfg.moe_intermediate_size
+    if reserve_bytes is None:
+        kv_tokens = ecfg.max_num_seqs * 4096
+        reserve_bytes = 24e9 + kv_tokens * cfg.kv_cache_dim * cfg.num_hidden_layers
+    sets = ecfg.weight_sets if ecfg.weight_sets > 0 else auto_weight_sets(cfg, ps, reserve_bytes, dev)
+    fp4 = cfg.expert_format == "nvfp4"
+    expert_sets = []
+    for s in range(min(sets, max(n_moe, 1))):
+        if fp4:
+            w13, w2 = rand_nvfp4(per, 2 * I, h, dev, sd), rand_nvfp4(per, h, I, dev, sd)
+        else:
+            w13, w2 = rand_mx((per,), 2 * I, h, dev, sd), rand_mx((per,), h, I, dev, sd)
+        expert_sets.append(ExpertWeights(first=first, count=per, w13=w13, w2=w2, inter=I, tiled=per <= 64))
+    layers = []
+    moe_idx = 0
+    for i in range(cfg.num_hidden_layers):
+        aw = V4AttnWeights(wqkv_a=Linear(rand_mx((), cfg.q_lora_rank + L, h, dev, sd)), q_norm=ones(cfg.q_lora_rank),
+                           kv_norm=ones(L), wq_b=Linear(rand_mx((), Hl * L, cfg.q_lora_rank, dev, sd)),
+                           wo_a=rand_bf16((Gl, R, (H // G) * L), dev, gen),
+                           wo_b=Linear(rand_mx((), h, Gl * R, dev, sd)),
+                           sink=rand_bf16((Hl,), dev, gen, std=1.0, dtype=torch.float32) if cfg.attn_sink else None)
+        if cfg.is_moe_layer(i):
+            sgu = sdn = None
+            if cfg.n_shared_experts:
+                si = cfg.moe_intermediate_size * cfg.n_shared_experts // tp
+                sgu, sdn = Linear(_gate_up(si, h, dev, sd)), Linear(rand_mx((), h, si, dev, sd))
+            ffn = MoEWeights(gate=rand_bf16((cfg.n_routed_experts, h), dev, gen, dtype=torch.float32),
+                             bias=torch.zeros(cfg.n_routed_experts, device=dev),
+                             experts=expert_sets[moe_idx % len(expert_sets)], shared_gate_up=sgu, shared_down=sdn)
+            moe_idx += 1
+        else:
+            Id = cfg.intermediate_size // tp
+            ffn = DenseWeights(gate_up=Linear(_gate_up(Id, h, dev, sd)), down=Linear(rand_mx((), h, Id, dev, sd)))
+        eng = None
+        if i in cfg.engram_layers:
+            rows = cfg.engram_rows // tp
+            cpu_gen = torch.Generator().manual_seed(seed * 7 + i * 131 + tr)
+            table = torch.randint(0, 256, (rows, cfg.engram_dim), dtype=torch.uint8, generator=cpu_gen) & 0xBF
+            scale = torch.full((rows, cfg.engram_dim // 32), SCALE_BYTE, dtype=torch.uint8)
+            eng = EngramWeights(table=host_mapped_copy(table), scale=host_mapped_copy(scale), row_lo=tr * rows,
+                                wkv=Linear(rand_mx((), 2 * h, cfg.engram_heads * cfg.engram_dim, dev, sd)),
+                                q_w=ones(h), k_w=ones(h))
+        layers.append(V4LayerWeights(attn_hc=hcw(M), ffn_hc=hcw(M), in_ln=ones(h), post_ln=ones(h), attn=aw,
+                                     ffn=ffn, engram=eng))
+    embed = rand_bf16((cfg.vocab_size, h), dev, gen)
+    v_local = -(-cfg.vocab_size // tp)
+    head = rand_mx((), v_local, h, dev, sd)
+    m = DeepseekV4Model(cfg, ecfg, ps, layers, embed, hcw(hc), ones(h), head, dev, kv_dtype=torch.float8_e4m3fn)
+    m.weight_sets = len(expert_sets)
+    return m

@@ -750,16 +750,22 @@ def kv_store_v4(kv, w, eps, table, pos, cache, slots, kv_scale, rd):
 
 
 def mqa_attention(q, cache, kv_scale, fb, softmax_scale, page_size, sink, table, rd, topk=None):
+    """Heads per rank below a multiple of 16 (e.g. 64 heads over 8 ranks) are
+    padded with zero queries up to the latent-attention kernel's head block;
+    the padded heads' outputs are dropped."""
     T, H, L = q.shape
     dev = q.device
-    q8 = torch.empty(T, H, 576, dtype=torch.uint8, device=dev)
-    qs = torch.empty(T, H, dtype=torch.float32, device=dev)
+    Hp = -(-H // 16) * 16
+    q8 = (torch.zeros if Hp != H else torch.empty)(T, Hp, 576, dtype=torch.uint8, device=dev)
+    qs = (torch.ones if Hp != H else torch.empty)(T, Hp, dtype=torch.float32, device=dev)
     qb = q if q.dtype == torch.bfloat16 else q.to(torch.bfloat16)
     _C.mqa_q_prep(qb, fb.positions, table, rd, q8, qs)
-    lse = torch.empty(T, H, dtype=torch.float32, device=dev) if sink is not None else None
+    lse = torch.empty(T, Hp, dtype=torch.float32, device=dev) if sink is not None else None
     out = _mla_core(q8, qs, cache, kv_scale, fb, softmax_scale, page_size, topk, lse_out=lse)
+    if Hp != H and sink is not None:
+        sink = torch.cat([sink.float(), sink.new_zeros(Hp - H)])
     _C.attn_fixup(out, lse, sink, rd, fb.positions, table)
-    return out
+    return out if Hp == H else out[:, :H].contiguous()
 
 
 def e5_prune(w, ids, cfg, n_experts):

@@ -118,7 +118,8 @@ def parse():
     p.add_argument("--config", default="v3-1k", choices=sorted(BENCH_CONFIGS),
                    help="named workload: v3-1k (headline: 671B, 64 x 1K, TP attention + EP), v32-sparse-32k "
                         "(671B + lightning indexer top-2048, 8 x 32K), v3-dp-2k / v3-nvfp4-dp-2k (DP attention "
-                        "+ EP, 256 x 2K; MXFP8 / NVFP4 routed experts)")
+                        "+ EP, 256 x 2K; MXFP8 / NVFP4 routed experts), v41-flash-1k (V4.1-Flash-shaped, "
+                        "64 x 1K)")
     p.add_argument("--model", default=None)
     p.add_argument("--batch", type=int, default=None)
     p.add_argument("--input-len", type=int, default=None)
@@ -139,6 +140,8 @@ BENCH_CONFIGS = {
     # DP attention on every rank + EP over all ranks, 256 requests x 2K
     "v3-dp-2k": {"model": "deepseek-v3-671b", "batch": 256, "input_len": 2048, "dp": True},
     "v3-nvfp4-dp-2k": {"model": "deepseek-v3-671b-nvfp4", "batch": 256, "input_len": 2048, "dp": True},
+    # the reference's served architecture: DeepSeek-V4.1-Flash shape (mHC, MQA + sinks, Engram, E5), NVFP4 experts
+    "v41-flash-1k": {"model": "deepseek-v4.1-flash", "batch": 64, "input_len": 1024},
 }
 
 
@@ -187,7 +190,11 @@ def main():
     log(f"building {args.model} on {world} GPU(s)")
     kv_per_tok = cfg.num_hidden_layers * (cfg.kv_cache_dim + (cfg.index_head_dim + 4 if cfg.index_n_heads else 0))
     reserve = 24e9 + local_batch * (ctx + 64) * kv_per_tok
-    model = build_random_model(cfg, ecfg, ps, dev, seed=0, reserve_bytes=reserve)
+    if cfg.is_v4:
+        from b200ds.models.random_init import build_random_model_v4
+        model = build_random_model_v4(cfg, ecfg, ps, dev, seed=0, reserve_bytes=reserve)
+    else:
+        model = build_random_model(cfg, ecfg, ps, dev, seed=0, reserve_bytes=reserve)
     torch.cuda.synchronize()
     t_init = time.time() - t0
     pages_per_seq = (ctx + ecfg.page_size - 1) // ecfg.page_size

@@ -275,6 +275,63 @@ def run_norm(T: int, iters: int, h=7168):
     report("add_rmsnorm_quant", f"T={T} h={h}", t, nbytes=T * h * (2 + 4 + 4 + 1 + 2))
 
 
+def run_v4(T: int, iters: int, D: int = 5120, H: int = 64, ctx: int = 1040):
+    """DeepSeek-V4.1-Flash-shaped decode-step kernels: mHC post, stats GEMM +
+    coefficient / combine / norm / quant, MQA with sinks (64 heads over the
+    latent rows), Engram gather from mapped host memory, E5 prune."""
+    from types import SimpleNamespace
+    from b200ds import _C, ops
+    from b200ds.config import v41_flash_config
+    from b200ds.models.deepseek_v4 import host_mapped_copy
+    from b200ds.models.rope import cos_sin_table
+    from b200ds.ops import HcWeights, cuda
+    cfg = v41_flash_config()
+    dev = torch.device("cuda")
+    X = torch.randn(T, 4, D, device=dev).to(torch.bfloat16)
+    y = torch.randn(T, D, device=dev).to(torch.bfloat16)
+    post = torch.rand(T, 4, device=dev)
+    comb = torch.rand(T, 16, device=dev) * 0.5
+    t = timed(lambda: cuda.hc_post(X, y, post, comb), iters)
+    report("v4_hc_post", f"T={T} hc=4 D={D}", t, nbytes=T * D * 2 * (4 + 4 + 1))
+    hw = HcWeights(torch.randn(24, 4 * D, device=dev) * 0.02, torch.ones(3, device=dev), torch.zeros(24, device=dev))
+    hw.fn_parts = cuda.hc_fn_parts(hw.fn)
+    ss = X.float().pow(2).sum((1, 2))
+    w = torch.ones(D, device=dev)
+
+    class _Q:
+        quantized = True
+    t = timed(lambda: cuda.hc_pre(X, ss, hw, w, 1e-6, cfg, _Q(), False, False), iters)
+    report("v4_hc_pre", f"T={T} hc=4 D={D} (stats GEMM + coeff/Sinkhorn/combine/norm/MXFP8)", t,
+           nbytes=T * 4 * D * 2 * 2 + 128 * 4 * D * 2 + T * D, note="3 launches incl. the zeroed raw buffer")
+    ps = 64
+    pages = (ctx + ps - 1) // ps
+    table = cos_sin_table(cfg, 4096, device=dev)
+    bt = (torch.arange(T * pages, dtype=torch.int32, device=dev).view(T, pages) + 1)
+    cache = torch.empty((T * pages + 1) * ps, 576, dtype=torch.uint8, device=dev)
+    _C.fill_bytes(cache, 7, 0xBF, 0)
+    cache = cache.view(torch.float8_e4m3fn)
+    q = (torch.randn(T, H, 512, device=dev) * 0.3).to(torch.bfloat16)
+    fb = SimpleNamespace(block_table=bt, q_seq=torch.arange(T, dtype=torch.int32, device=dev),
+                         positions=torch.full((T,), ctx - 1, dtype=torch.int32, device=dev), is_decode=True,
+                         max_seq_len=ctx)
+    sink = torch.randn(H, device=dev)
+    t = timed(lambda: ops.mqa_attention(q, cache, 1.0, fb, cfg.softmax_scale, ps, sink, table, 64), iters)
+    report("v4_mqa_sink", f"B={T} ctx={ctx} H={H} (q prep + latent attention + sink/inverse-rope fix-up)", t,
+           nbytes=T * ctx * 576 + T * H * 512 * 2 * 2, flops=2 * T * H * ctx * (512 + 512))
+    rows = 1 << 20
+    tab = host_mapped_copy(torch.randint(0, 256, (rows, 256), dtype=torch.uint8) & 0xBF)
+    sc = host_mapped_copy(torch.full((rows, 8), 122, dtype=torch.uint8))
+    ids = torch.randint(0, rows, (T, 100), dtype=torch.int32, device=dev)
+    out = torch.empty(T * 100, 256, dtype=torch.bfloat16, device=dev)
+    t = timed(lambda: _C.engram_gather(tab, sc, ids, 0, out), iters)
+    report("v4_engram_gather", f"T={T} x 100 heads from mapped host memory", t, nbytes=T * 100 * (256 + 8),
+           note="host-link bound")
+    wts = torch.rand(T, 6, device=dev)
+    eids = torch.randint(0, 384, (T, 6), dtype=torch.int32, device=dev)
+    t = timed(lambda: cuda.e5_prune(wts.clone(), eids.clone(), cfg, 384), iters)
+    report("v4_e5_prune", f"T={T} top6 of 384", t, note="includes two input copies")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="")
@@ -319,6 +376,7 @@ def main():
         ("gemm_o_proj_T64", lambda: run_gemm("o_proj", 64, 7168, 16384, a.iters)),
         ("gemm_o_proj_tp8_T64", lambda: run_gemm("o_proj_tp8", 64, 7168, 2048, a.iters)),
         ("add_rmsnorm_quant_T64", lambda: run_norm(64, a.iters)),
+        ("v4_T64", lambda: run_v4(64, a.iters)),
     ]
     for name, fn in cases:
         if a.only and a.only not in name:

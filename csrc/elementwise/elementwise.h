@@ -64,8 +64,8 @@ int b200_hc_embed(const void* embed, const int* ids, int T, int hc, int D, void*
 int b200_kv_store_v4(const void* kv, int f32, int64_t ld, int T, int L, int rd, const float* w, float eps,
                      const int* pos, const float* table, const int64_t* slots, uint8_t* cache, float kv_scale,
                      cudaStream_t st);
-int b200_mqa_q_prep(const void* q, int64_t qt, int64_t qh, int T, int H, int rd, const int* pos, const float* table,
-                    uint8_t* q8, float* qs, cudaStream_t st);
+int b200_mqa_q_prep(const void* q, int64_t qt, int64_t qh, int T, int H, int Hq, int rd, const int* pos,
+                    const float* table, uint8_t* q8, float* qs, cudaStream_t st);
 int b200_attn_fixup(void* o, int T, int H, const float* lse, const float* sink, int rd, const int* pos,
                     const float* table, cudaStream_t st);
 int b200_e5_prune(int* ids, float* w, int T, int K, int E, float budget, int max_count, cudaStream_t st);

@@ -414,7 +414,9 @@ __global__ void __launch_bounds__(128) kv_store_v4_kernel(const void* kv, int f3
 }
 
 // one warp per (token, head); 16 consecutive elements per lane (L = 512)
-__global__ void mqa_q_prep_kernel(const __nv_bfloat16* q, int64_t qt, int64_t qh, int T, int H, int rd,
+// q8 / qs hold Hq >= H heads per token (extra heads stay as the caller set
+// them: zero queries that pad H to the attention kernel's head block)
+__global__ void mqa_q_prep_kernel(const __nv_bfloat16* q, int64_t qt, int64_t qh, int T, int H, int Hq, int rd,
                                   const int* pos, const float* table, uint8_t* q8, float* qs) {
   pdl_wait();
   if (threadIdx.x == 0) pdl_launch_dependents();
@@ -444,7 +446,8 @@ __global__ void mqa_q_prep_kernel(const __nv_bfloat16* q, int64_t qt, int64_t qh
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   const float sc = amax > 0.f ? amax / 448.f : 1.f;
   const float inv = 1.f / sc;
-  uint8_t* dst = q8 + (int64_t)w * kRow;
+  const int64_t wq = (int64_t)t * Hq + h;
+  uint8_t* dst = q8 + wq * kRow;
   uint32_t packed[E / 4];
 #pragma unroll
   for (int i = 0; i < E; i += 4) {
@@ -453,7 +456,7 @@ __global__ void mqa_q_prep_kernel(const __nv_bfloat16* q, int64_t qt, int64_t qh
   }
   *reinterpret_cast<uint4*>(dst + lane * E) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
   reinterpret_cast<uint16_t*>(dst + L)[lane] = 0;      // no separate rope key: zero query part
-  if (lane == 0) qs[w] = sc;
+  if (lane == 0) qs[wq] = sc;
 }
 
 __global__ void attn_fixup_kernel(__nv_bfloat16* o, int T, int H, const float* lse, const float* sink, int rd,
@@ -630,13 +633,13 @@ int b200_kv_store_v4(const void* kv, int f32, int64_t ld, int T, int L, int rd, 
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
 
-int b200_mqa_q_prep(const void* q, int64_t qt, int64_t qh, int T, int H, int rd, const int* pos, const float* table,
-                    uint8_t* q8, float* qs, cudaStream_t st) {
+int b200_mqa_q_prep(const void* q, int64_t qt, int64_t qh, int T, int H, int Hq, int rd, const int* pos,
+                    const float* table, uint8_t* q8, float* qs, cudaStream_t st) {
   if (T <= 0) return 0;
-  if (rd % 16 || rd > 512 || qt % 8 || qh % 8) return -1;
+  if (rd % 16 || rd > 512 || qt % 8 || qh % 8 || Hq < H) return -1;
   const int warps = T * H;
   b200::launch_pdl(mqa_q_prep_kernel, dim3((warps * 32 + 255) / 256), dim3(256), 0, st,
-                   reinterpret_cast<const __nv_bfloat16*>(q), qt, qh, T, H, rd, pos, table, q8, qs);
+                   reinterpret_cast<const __nv_bfloat16*>(q), qt, qh, T, H, Hq, rd, pos, table, q8, qs);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
 

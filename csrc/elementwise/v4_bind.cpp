@@ -130,7 +130,10 @@ void mqa_q_prep(const at::Tensor& q, const at::Tensor& pos, const at::Tensor& ta
   TORCH_CHECK(q.is_cuda() && q.dim() == 3 && q.size(2) == 512 && q.stride(2) == 1 && q.scalar_type() == at::kBFloat16,
               "q bf16 [T, H, 512]");
   const c10::cuda::CUDAGuard g(q.device());
-  chk(b200_mqa_q_prep(q.data_ptr(), q.stride(0), q.stride(1), q.size(0), q.size(1), rd, pos.data_ptr<int>(),
+  TORCH_CHECK(q8.dim() == 3 && q8.size(0) == q.size(0) && q8.size(1) >= q.size(1) && q8.size(2) == 576 &&
+                  qs.numel() >= q8.size(0) * q8.size(1),
+              "q8 [T, Hq >= H, 576], qs [T, Hq]");
+  chk(b200_mqa_q_prep(q.data_ptr(), q.stride(0), q.stride(1), q.size(0), q.size(1), q8.size(1), rd, pos.data_ptr<int>(),
                       table.data_ptr<float>(), reinterpret_cast<uint8_t*>(q8.data_ptr()), qs.data_ptr<float>(), cur()),
       "mqa_q_prep");
 }
