@@ -100,7 +100,7 @@ struct Tile {
 // The routing layout (tile offsets, segment starts / counts) is staged in
 // shared memory once per CTA: sm_lay[0..E] = ttile_off, [E+1..2E] =
 // seg_start, [2E+1..3E] = seg_count.
-constexpr int kMaxExperts = 256;
+constexpr int kMaxExperts = 512;   // local experts per GPU (V4.1-Flash: 384 on one GPU)
 __device__ __forceinline__ Tile map_tile(const Params& p, const int* lay, int w) {
   Tile t;
   const int ttg = w / p.n_tiles;

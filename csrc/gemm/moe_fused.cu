@@ -33,7 +33,7 @@ constexpr int kTileM = 128;
 constexpr int kTileK = 128;
 constexpr int kSf = 512;
 constexpr int kRing = 4;
-constexpr int kMaxExperts = 256;
+constexpr int kMaxExperts = 512;   // local experts per GPU (V4.1-Flash: 384 on one GPU)
 
 template <int BN, bool FP4>
 struct Cfg {
