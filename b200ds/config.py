@@ -305,3 +305,4 @@ class EngineConfig:
     weight_sets: int = 0             # >0: cycle this many distinct layer weight sets (when the model exceeds HBM)
     spec_ngram: int = 0              # >0: speculative decoding with n-gram (prompt lookup) drafts up to this n
     spec_k: int = 4                  # draft tokens verified per step
+    selfcheck: bool = True           # GPU: check each switchable fast path once at start (fail-closed, ranks agree)

@@ -72,6 +72,14 @@ class Engine:
         # each step on the mode and on the per-rank token rows of the MoE
         # exchange (gloo, host only), and an idle rank joins with a dummy.
         self.dp = bool(ecfg.dp_attention) and self.ps.ep_size > 1
+        self.selfcheck = {}
+        if self.device.type == "cuda" and ecfg.selfcheck:
+            from .. import ops
+            if ops.get_impl() == "native":
+                from ..ops import cuda as _cuda
+                from ..utils import levers
+                _cuda.register_selfchecks()
+                self.selfcheck = levers.selfcheck(getattr(self.ps, "cpu_group", None))
 
     def _auto_pages(self) -> int:
         if self.device.type != "cuda":

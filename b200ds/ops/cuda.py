@@ -12,6 +12,7 @@ from typing import Optional
 import torch
 import torch.distributed as dist
 
+from ..utils import levers
 from .quant import MXFP8Tensor, round_up
 
 try:
@@ -326,18 +327,14 @@ def moe_tile_n(rows_per_expert: float, cap: int) -> int:
     return cap
 
 
-MOE_FUSED = os.environ.get("B200_MOE_FUSED", "1") != "0"
-# the fused kernel reads FC1 rows straight from the activations / dispatch
-# buffer (no expert-sorted copy); 0 keeps the separate gather for comparison
-MOE_PULL = os.environ.get("B200_MOE_PULL", "1") != "0"
-
-
 def _fused(bn1: int, bn2: int) -> bool:
-    return MOE_FUSED and bn1 == bn2
+    return levers.on("moe_fused") and bn1 == bn2
 
 
 def _pulls(bn1: int, bn2: int) -> bool:
-    return MOE_PULL and _fused(bn1, bn2)
+    """The fused kernel reads FC1 rows straight from the activations /
+    dispatch buffer (switch moe_pull; off keeps the separate gather)."""
+    return levers.on("moe_pull") and _fused(bn1, bn2)
 
 
 def _moe_ws(ex, dev) -> torch.Tensor:
@@ -794,3 +791,54 @@ def engram_update(X, ids, ew, cfg, ps):
     ss = torch.empty(T, dtype=torch.float32, device=X.device)
     _C.engram_gate(X, kv, ew.q_w, ew.k_w, cfg.rms_norm_eps, cfg.engram_clamp, ss)
     return ss
+
+
+# ---------------------------------------------------------------------------
+# self-checks of the switchable fast paths (run once at engine start)
+# ---------------------------------------------------------------------------
+
+def _moe_check_case():
+    from . import ExpertWeights
+    g = torch.Generator(device="cuda").manual_seed(11)
+    E, H, I, K, T = 8, 512, 256, 2, 24
+
+    def mx(n, k):
+        a = quant((torch.randn(E * n, k, device="cuda", generator=g) * 0.05).to(torch.bfloat16))
+        return MXFP8Tensor(a.q.view(E, n, k), a.sf.view(E, -1), n)
+    ex = ExpertWeights(0, E, mx(2 * I, H), mx(H, I), I)
+    x = quant(torch.randn(T, H, device="cuda", generator=g).to(torch.bfloat16))
+    ids = torch.stack([torch.randperm(E, device="cuda", generator=g)[:K] for _ in range(T)]).int()
+    w = torch.rand(T, K, device="cuda", generator=g)
+    return ex, x, ids, w
+
+
+def _check_moe(switch: str) -> bool:
+    """moe_fused: one persistent launch == the two grouped launches;
+    moe_pull: in-place row reads == the pre-gathered operand (bitwise)."""
+    ex, x, ids, w = _moe_check_case()
+    keep = {n: levers.on(n) for n in ("moe_fused", "moe_pull")}
+    try:
+        if switch == "moe_fused":
+            levers.set_switch("moe_fused", False)
+            ref_out = moe_experts(x, w, ids, ex, torch.float32)
+            levers.set_switch("moe_fused", True)
+            levers.set_switch("moe_pull", False)
+        else:
+            levers.set_switch("moe_fused", True)
+            levers.set_switch("moe_pull", False)
+            ref_out = moe_experts(x, w, ids, ex, torch.float32)
+            levers.set_switch("moe_pull", True)
+        out = moe_experts(x, w, ids, ex, torch.float32)
+        torch.cuda.synchronize()
+        check_device_errors()
+        return bool(torch.equal(out, ref_out))
+    finally:
+        for n, v in keep.items():
+            levers.set_switch(n, v)
+
+
+def register_selfchecks() -> None:
+    for name in ("moe_fused", "moe_pull"):
+        sw = levers._REGISTRY[name]
+        if not sw.checks:
+            levers.add_check(name, lambda n=name: _check_moe(n))

@@ -318,6 +318,8 @@ def main():
                        "context_during_timing": [args.input_len + args.warmup, args.input_len + args.warmup + 2 * args.steps],
                        "parallelism": (f"dp{world}-attn+ep{world}-moe" if args.dp else f"tp{world}-attn+ep{world}-moe"),
                        "expert_format": cfg.expert_format, "weight_sets": getattr(model, "weight_sets", None),
+                       "switches": __import__("b200ds.utils.levers", fromlist=["switches"]).switches(),
+                       "selfcheck": eng.selfcheck,
                        "l2": "no flush: per-step weights+KV >> 126 MB L2", "init_s": round(t_init, 1)},
         }
         print(json.dumps(out), flush=True)

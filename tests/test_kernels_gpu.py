@@ -580,17 +580,20 @@ def test_moe_fused_matches_two_launch(fp4, tiled, T, skew):
     wts = torch.rand(T, K, device=DEV)
     run = (lambda: cuda.moe_experts_nvfp4(x, wts, ids, ex, torch.float32)) if fp4 else \
         (lambda: cuda.moe_experts(cuda.quant(x), wts, ids, ex, torch.float32))
-    old = cuda.MOE_FUSED, cuda.MOE_PULL
+    from b200ds.utils import levers
+    old = levers.on("moe_fused"), levers.on("moe_pull")
     try:
-        cuda.MOE_FUSED = False
+        levers.set_switch("moe_fused", False)
         a = run()
-        cuda.MOE_FUSED, cuda.MOE_PULL = True, False
+        levers.set_switch("moe_fused", True)
+        levers.set_switch("moe_pull", False)
         d = run()                  # fused, rows gathered into a sorted copy first
-        cuda.MOE_PULL = True
+        levers.set_switch("moe_pull", True)
         b = run()                  # fused, producer reads the rows in place
         c = run()                  # counters reset by the previous launch
     finally:
-        cuda.MOE_FUSED, cuda.MOE_PULL = old
+        levers.set_switch("moe_fused", old[0])
+        levers.set_switch("moe_pull", old[1])
     torch.cuda.synchronize()
     cuda.check_device_errors()
     assert torch.equal(a, d) and torch.equal(a, b) and torch.equal(b, c)
