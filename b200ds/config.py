@@ -306,3 +306,4 @@ class EngineConfig:
     spec_ngram: int = 0              # >0: speculative decoding with n-gram (prompt lookup) drafts up to this n
     spec_k: int = 4                  # draft tokens verified per step
     selfcheck: bool = True           # GPU: check each switchable fast path once at start (fail-closed, ranks agree)
+    trace: bool = False              # device timestamps per layer phase (also B200_TRACE=1); adds launches

@@ -93,6 +93,8 @@ class DecodeGraphRunner:
         with torch.cuda.graph(g.graph, pool=self.pool):
             g.tokens = self.model.forward_tokens(g.fb, g.temp, g.top_p, g.top_k, g.unif)
         g.graph.instantiate()
+        tr = getattr(self.model, "tracer", None)
+        g.trace_names = list(tr.names) if tr is not None and tr.enabled else []
         self.graphs[bs] = g
         return g
 

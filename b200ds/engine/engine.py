@@ -72,6 +72,10 @@ class Engine:
         # each step on the mode and on the per-rank token rows of the MoE
         # exchange (gloo, host only), and an idle rank joins with a dummy.
         self.dp = bool(ecfg.dp_attention) and self.ps.ep_size > 1
+        import os
+        if ecfg.trace or os.environ.get("B200_TRACE", "0") == "1":
+            from ..utils.trace import Tracer
+            model.tracer = Tracer(self.device, enabled=True)
         self.selfcheck = {}
         if self.device.type == "cuda" and ecfg.selfcheck:
             from .. import ops

@@ -116,6 +116,8 @@ class DeepseekModel:
         self.ix_cache: List[torch.Tensor] = []
         self.ix_scale: List[torch.Tensor] = []
         self.page_size = ecfg.page_size
+        from ..utils.trace import null_tracer
+        self.tracer = null_tracer()       # the engine installs a Tracer when tracing is on
         if self.device.type == "cuda":
             for lw in layers:       # [H, L, nope] copy of W_uk for the tensor-core absorption
                 w = lw.attn.w_uk
@@ -299,12 +301,17 @@ class DeepseekModel:
     def _hidden(self, fb: ForwardBatch):
         """All decoder layers + the final norm; returns the normed hidden."""
         c = self.cfg
+        tr = self.tracer
+        tr.reset()
+        tr.mark("embed")
         residual = self.embed[fb.input_ids.long()].float()      # fp32 residual stream
         h = ops.rmsnorm_act(residual, self.layers[0].in_ln, c.rms_norm_eps, self.layers[0].attn.qkv_a)
         for i, lw in enumerate(self.layers):
+            tr.mark(f"L{i}.attn")
             a = self._attention(i, lw, h, fb)
             h, residual = ops.allreduce_add_rmsnorm(a, residual, lw.post_ln, c.rms_norm_eps,
                                                     self.ps, "tp_attn", self._ffn_first_linear(lw))
+            tr.mark(f"L{i}.ffn")
             f = self._ffn(i, lw, h, fb)
             nxt = self.layers[i + 1] if i + 1 < len(self.layers) else None
             # under DP attention only the fused expert-parallel partial still
@@ -313,6 +320,7 @@ class DeepseekModel:
             h, residual = ops.allreduce_add_rmsnorm(
                 f, residual, nxt.in_ln if nxt else self.final_ln, c.rms_norm_eps, ps_f,
                 "ffn", nxt.attn.qkv_a if nxt else None)
+        tr.mark("head")
         return h
 
     def _last_hidden(self, h, fb: ForwardBatch) -> torch.Tensor:
@@ -334,7 +342,9 @@ class DeepseekModel:
         logits: returns token ids [B] (greedy for rows with temperature <= 0)."""
         h = self._hidden(fb)
         local = ops.lm_head_local(self._last_hidden(h, fb), self.lm_head)
-        return ops.sample_tokens(local, self.vocab_offset(), temperature, top_p, top_k, uniform, self.ps)
+        out = ops.sample_tokens(local, self.vocab_offset(), temperature, top_p, top_k, uniform, self.ps)
+        self.tracer.mark("end")
+        return out
 
     def _ffn_first_linear(self, lw: LayerWeights):
         if isinstance(lw.ffn, DenseWeights):

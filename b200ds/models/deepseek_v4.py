@@ -86,6 +86,8 @@ class DeepseekV4Model:
         self.tok_cache: Optional[torch.Tensor] = None
         self.page_size = ecfg.page_size
         self.aux: List[torch.Tensor] = []
+        from ..utils.trace import null_tracer
+        self.tracer = null_tracer()
         from ..ops.ref import engram_multipliers
         m = [v - (1 << 64) if v >= (1 << 63) else v for v in engram_multipliers(max(cfg.engram_heads, 1))]
         self.engram_mults = torch.tensor(m, dtype=torch.int64, device=self.device)
@@ -158,6 +160,9 @@ class DeepseekV4Model:
     def _hidden(self, fb: ForwardBatch):
         c = self.cfg
         eps = c.rms_norm_eps
+        tr = self.tracer
+        tr.reset()
+        tr.mark("embed")
         X, ss = ops.hc_embed(self.embed, fb.input_ids, c.hc_mult)
         eids = None
         if c.engram_layers:
@@ -165,6 +170,7 @@ class DeepseekV4Model:
         self.aux = []
         carry = None
         for i, lw in enumerate(self.layers):
+            tr.mark(f"L{i}.attn")
             if carry is not None:
                 ss = ops.hc_post(X, *carry)
             if lw.engram is not None:
@@ -174,10 +180,12 @@ class DeepseekV4Model:
             h, post, comb = ops.hc_pre(X, ss, lw.attn_hc, lw.in_ln, eps, c, lw.attn.wqkv_a)
             y = self._attention(i, lw, h, fb)
             ss = ops.hc_post(X, y, post, comb)
+            tr.mark(f"L{i}.ffn")
             moe = isinstance(lw.ffn, MoEWeights)
             h, post, comb = ops.hc_pre(X, ss, lw.ffn_hc, lw.post_ln, eps, c, self._ffn_first_linear(lw),
                                        keep_hf=moe)
             carry = (self._ffn(i, lw, h, fb), post, comb)
+        tr.mark("head")
         ss = ops.hc_post(X, *carry)
         h, _, _ = ops.hc_pre(X, ss, self.hc_head, self.final_ln, eps, c, None, head=True)
         return h
@@ -200,7 +208,9 @@ class DeepseekV4Model:
     def forward_tokens(self, fb: ForwardBatch, temperature, top_p, top_k, uniform) -> torch.Tensor:
         h = self._hidden(fb)
         local = ops.lm_head_local(self._last_hidden(h, fb), self.lm_head)
-        return ops.sample_tokens(local, self.vocab_offset(), temperature, top_p, top_k, uniform, self.ps)
+        out = ops.sample_tokens(local, self.vocab_offset(), temperature, top_p, top_k, uniform, self.ps)
+        self.tracer.mark("end")
+        return out
 
 
 # ---------------------------------------------------------------------------

@@ -124,6 +124,9 @@ def parse():
     p.add_argument("--batch", type=int, default=None)
     p.add_argument("--input-len", type=int, default=None)
     p.add_argument("--weight-sets", type=int, default=0)
+    p.add_argument("--trace", action="store_true",
+                   help="device timestamps per layer phase inside the decode graph (adds launches: the step "
+                        "time of a traced run is not a clean measurement); adds a per-phase breakdown to the JSON")
     a = p.parse_args()
     d = BENCH_CONFIGS[a.config]
     a.model = a.model or d["model"]
@@ -185,7 +188,7 @@ def main():
     ecfg = EngineConfig(tp_size=1 if args.dp else world, ep_size=world, page_size=64, max_num_seqs=local_batch,
                         max_prefill_tokens=16384 if not args.dp else 4096, cuda_graphs=True,
                         graph_batch_sizes=(local_batch,), enable_prefix_cache=False, weight_sets=args.weight_sets,
-                        max_model_len=max(16384, ctx + 64), dp_attention=args.dp)
+                        max_model_len=max(16384, ctx + 64), dp_attention=args.dp, trace=args.trace)
     t0 = time.time()
     log(f"building {args.model} on {world} GPU(s)")
     kv_per_tok = cfg.num_hidden_layers * (cfg.kv_cache_dim + (cfg.index_head_dim + 4 if cfg.index_n_heads else 0))
@@ -265,6 +268,13 @@ def main():
         barrier()
     dev_ms = max_over_ranks(e0.elapsed_time(e1))
     step_ms = dev_ms / args.steps
+    trace_us = None
+    if args.trace and gr.trace_names:
+        tr = model.tracer
+        gr.graph.replay()
+        st = tr.stamps()
+        tr.names = gr.trace_names
+        trace_us = {k: round(v, 1) for k, v in tr.summary(st).items()}
     value = args.batch * args.steps / (dev_ms / 1e3)
 
     log(f"device-timed {step_ms:.2f} ms/step; e2e")
@@ -322,6 +332,8 @@ def main():
                        "selfcheck": eng.selfcheck,
                        "l2": "no flush: per-step weights+KV >> 126 MB L2", "init_s": round(t_init, 1)},
         }
+        if trace_us is not None:
+            out["trace_us_per_step"] = trace_us      # traced run: timing includes the stamp launches
         print(json.dumps(out), flush=True)
     # Teardown: drop every reference to the captured graphs (they hold NCCL
     # work) before the process group goes; a watchdog ends the process if the

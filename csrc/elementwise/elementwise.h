@@ -69,3 +69,7 @@ int b200_mqa_q_prep(const void* q, int64_t qt, int64_t qh, int T, int H, int Hq,
 int b200_attn_fixup(void* o, int T, int H, const float* lse, const float* sink, int rd, const int* pos,
                     const float* table, cudaStream_t st);
 int b200_e5_prune(int* ids, float* w, int T, int K, int E, float budget, int max_count, cudaStream_t st);
+
+// Tracing (see trace.cu): %globaltimer into buf[idx] once the stream's
+// previous kernel has completed.
+int b200_trace_stamp(void* buf, int idx, cudaStream_t st);

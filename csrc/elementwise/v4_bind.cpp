@@ -156,9 +156,16 @@ void e5_prune(at::Tensor ids, at::Tensor w, int64_t E, double budget, int64_t ma
       "e5_prune");
 }
 
+void trace_stamp(at::Tensor buf, int64_t idx) {
+  TORCH_CHECK(buf.is_cuda() && buf.scalar_type() == at::kLong && idx >= 0 && idx < buf.numel(), "buf int64 [n]");
+  const c10::cuda::CUDAGuard g(buf.device());
+  chk(b200_trace_stamp(buf.data_ptr(), int(idx), cur()), "trace_stamp");
+}
+
 }  // namespace
 
 void register_v4(pybind11::module& m) {
+  m.def("trace_stamp", &trace_stamp);
   m.def("hc_post", &hc_post);
   m.def("hc_pre", &hc_pre);
   m.def("hc_mean", &hc_mean);
