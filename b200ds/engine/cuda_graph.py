@@ -167,3 +167,111 @@ class DecodeGraphRunner:
         """Drop the graphs (before destroying the process group)."""
         self.graphs.clear()
         self.pool = None
+
+
+def build_verify_batch(seqs: List[dict], k: int, rows: int, page_size: int, max_pages: int) -> ForwardBatch:
+    """Speculative-verify batch in a fixed layout: `rows` requests x (1 + k)
+    token rows.  Request i occupies rows [i (1 + k), (i + 1)(1 + k)): its
+    newest token, its draft, then padding.  Padding rows repeat the last
+    real position (so they only read pages the request owns) and write their
+    latent to the scratch slot 0 of reserved page 0, so they never touch live
+    KV; absent requests are all-padding rows on page 0.  All rows return
+    logits.  Host tensors (CPU)."""
+    w = 1 + k
+    T = rows * w
+    ids = torch.zeros(T, dtype=torch.int32)
+    pos = torch.zeros(T, dtype=torch.int32)
+    qs = torch.arange(rows, dtype=torch.int32).repeat_interleave(w)
+    slots = torch.zeros(T, dtype=torch.int64)
+    lens = torch.ones(rows, dtype=torch.int32)
+    bt = torch.zeros(rows, max_pages, dtype=torch.int32)
+    for i, s in enumerate(seqs):
+        toks, st, pages = s["tokens"], s["start"], s["pages"]
+        if len(toks) > w:
+            raise ValueError("draft longer than spec_k")
+        if len(pages) > max_pages:
+            raise ValueError("sequence longer than EngineConfig.max_model_len")
+        for j in range(w):
+            r = i * w + j
+            if j < len(toks):
+                p = st + j
+                ids[r] = toks[j]
+                slots[r] = pages[p // page_size] * page_size + p % page_size
+            else:
+                p = st + len(toks) - 1       # padding: the last real position (pages exist up to it)
+            pos[r] = p
+        lens[i] = st + w
+        bt[i, : len(pages)] = torch.tensor(pages, dtype=torch.int32)
+    return ForwardBatch(input_ids=ids, positions=pos, q_seq=qs, out_slots=slots, seq_lens=lens, block_table=bt,
+                        last_idx=torch.arange(T, dtype=torch.int64), is_decode=False, max_q_len=w,
+                        max_seq_len=max_pages * page_size)
+
+
+class VerifyGraphRunner:
+    """CUDA graphs of the speculative-verify forward (fixed 1 + spec_k rows
+    per request, one graph per request bucket): logits at every row and the
+    greedy argmax on the device, only the token ids come back."""
+
+    def __init__(self, engine, k: int, batch_sizes=None, max_pages: Optional[int] = None):
+        self.eng = engine
+        self.model = engine.model
+        self.dev = engine.device
+        ecfg = engine.ecfg
+        self.k = k
+        self.page_size = ecfg.page_size
+        self.batch_sizes = sorted(batch_sizes or [b for b in ecfg.graph_batch_sizes if b <= ecfg.max_num_seqs])
+        if not self.batch_sizes or self.batch_sizes[-1] < ecfg.max_num_seqs:
+            self.batch_sizes.append(ecfg.max_num_seqs)
+        self.max_pages = max_pages or (ecfg.max_model_len + self.page_size - 1) // self.page_size
+        self.graphs: Dict[int, _Graph] = {}
+        self.pool = None
+
+    def can_run(self, n: int) -> bool:
+        return n <= self.batch_sizes[-1]
+
+    def _bucket(self, n: int) -> int:
+        for b in self.batch_sizes:
+            if b >= n:
+                return b
+        raise ValueError(n)
+
+    def _capture(self, bs: int) -> _Graph:
+        g = _Graph()
+        host = build_verify_batch([], self.k, bs, self.page_size, self.max_pages)
+        g.h = ForwardBatch(**{k: (v.pin_memory() if isinstance(v, torch.Tensor) else v)
+                              for k, v in host.__dict__.items()})
+        g.fb = ForwardBatch(**{k: (v.to(self.dev) if isinstance(v, torch.Tensor) else v)
+                               for k, v in host.__dict__.items()})
+        g.h_tok = torch.zeros(host.num_tokens, dtype=torch.int64).pin_memory()
+        s = torch.cuda.Stream(device=self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self.model.forward(g.fb).argmax(-1)
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        torch.cuda.synchronize(self.dev)
+        g.graph = torch.cuda.CUDAGraph()
+        if self.pool is None:
+            self.pool = torch.cuda.graph_pool_handle()
+        with torch.cuda.graph(g.graph, pool=self.pool):
+            g.tokens = self.model.forward(g.fb).argmax(-1)
+        self.graphs[bs] = g
+        return g
+
+    def run(self, seqs: List[dict]) -> List[int]:
+        """seqs: per request {"tokens": newest + draft, "start", "pages"};
+        returns the argmax token of every row, request-major (1 + k each)."""
+        bs = self._bucket(len(seqs))
+        g = self.graphs.get(bs) or self._capture(bs)
+        host = build_verify_batch(seqs, self.k, bs, self.page_size, self.max_pages)
+        for name in ("input_ids", "positions", "out_slots", "seq_lens", "block_table"):
+            getattr(g.h, name).copy_(getattr(host, name))
+            getattr(g.fb, name).copy_(getattr(g.h, name), non_blocking=True)
+        g.graph.replay()
+        g.h_tok.copy_(g.tokens, non_blocking=True)
+        torch.cuda.current_stream(self.dev).synchronize()
+        return g.h_tok.tolist()
+
+    def release(self) -> None:
+        self.graphs.clear()
+        self.pool = None

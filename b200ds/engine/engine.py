@@ -64,6 +64,7 @@ class Engine:
         self.tokenizer = tokenizer
         self._next_rid = 0
         self.graphs = None
+        self.verify_graphs, self.verify_graphs_ok = None, True
         if self.device.type == "cuda" and ecfg.cuda_graphs:
             from .cuda_graph import DecodeGraphRunner
             self.graphs = DecodeGraphRunner(self)
@@ -244,18 +245,43 @@ class Engine:
             return None
         seqs = [{"tokens": ch + d, "start": s, "pages": r.pages}
                 for r, ch, s, d in zip(st.reqs, st.chunks, st.starts, drafts)]
+        k = self.ecfg.spec_k
+        if self.graphs is not None and self.verify_graphs_ok:
+            # fixed (1 + spec_k) rows per request: one captured graph per bucket
+            if self.verify_graphs is None:
+                from .cuda_graph import VerifyGraphRunner
+                self.verify_graphs = VerifyGraphRunner(self, k, max_pages=self.graphs.max_pages)
+            if self.verify_graphs.can_run(len(seqs)):
+                try:
+                    pred = self.verify_graphs.run(seqs)
+                except RuntimeError as e:    # capture failed: verify eagerly from now on
+                    from ..utils import levers
+                    levers.announce("verify-graphs-off", f"verify graphs off ({e}); eager verify")
+                    self.verify_graphs.release()
+                    self.verify_graphs, self.verify_graphs_ok = None, False
+                else:
+                    starts = [i * (1 + k) for i in range(len(seqs))]
+                    return self._accept(st, drafts, pred, starts)
         fb = build_batch(seqs, self.ecfg.page_size, device="cpu")
         fb.last_idx = torch.arange(fb.num_tokens, dtype=torch.int64)     # logits at every position
         fb = self._to_device(fb)
         pred = self.model.forward(fb).argmax(-1).tolist()
-        out, off = [], 0
-        for r, d in zip(st.reqs, drafts):
+        starts, off = [], 0
+        for d in drafts:
+            starts.append(off)
+            off += 1 + len(d)
+        return self._accept(st, drafts, pred, starts)
+
+    def _accept(self, st: Step, drafts, pred: List[int], starts: List[int]) -> List[List[int]]:
+        """Greedy acceptance: the longest draft prefix the model reproduces,
+        then the model's own next token."""
+        out = []
+        for r, d, off in zip(st.reqs, drafts, starts):
             p = pred[off: off + 1 + len(d)]
             a = 0
             while a < len(d) and p[a] == d[a]:
                 a += 1
             out.append(d[:a] + [p[a]])
-            off += 1 + len(d)
             self.stats["spec_proposed"] = self.stats.get("spec_proposed", 0) + len(d)
             self.stats["spec_accepted"] = self.stats.get("spec_accepted", 0) + a
         return out
