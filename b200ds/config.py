@@ -52,6 +52,9 @@ class ModelConfig:
     index_n_heads: int = 0
     index_head_dim: int = 128
     index_topk: int = 2048
+    # sliding window always kept by the sparse selection (the last index_swa
+    # positions up to the query), on top of the indexer's top-k
+    index_swa: int = 0
     # Weight formats: "mxfp8" (e4m3 + UE8M0 per 32 along K), "nvfp4"
     # (e2m1 + e4m3 per 16 along K + fp32 global), "bf16" or "fp32".
     dense_format: str = "mxfp8"

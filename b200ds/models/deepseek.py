@@ -199,7 +199,7 @@ class DeepseekModel:
         ops.index_k_store(k_raw, aw.ix_k_norm_w, aw.ix_k_norm_b, 1e-6, self.rope_table, fb.positions,
                           self.ix_cache[i], self.ix_scale[i], fb.out_slots)
         return ops.indexer_topk(q_raw, w_raw, (nh * hd) ** -0.5, self.rope_table, self.ix_cache[i],
-                                self.ix_scale[i], fb, self.page_size, c.index_topk)
+                                self.ix_scale[i], fb, self.page_size, c.index_topk, c.index_swa)
 
     def _ffn(self, i: int, lw: LayerWeights, h, fb: ForwardBatch) -> torch.Tensor:
         c = self.cfg

@@ -52,6 +52,11 @@ class V4AttnWeights:
     wo_a: torch.Tensor            # [Gl, R, (H/G) * L]
     wo_b: Linear                  # [D, Gl * R]
     sink: Optional[torch.Tensor]  # [Hl]
+    # sparse attention: the lightning indexer's projections ride on the
+    # attention GEMMs (wk and weights_proj rows appended to wqkv_a, the
+    # indexer's wq_b rows to wq_b)
+    ix_k_norm_w: Optional[torch.Tensor] = None
+    ix_k_norm_b: Optional[torch.Tensor] = None
 
 
 @dataclass
@@ -98,12 +103,18 @@ class DeepseekV4Model:
         slots = num_pages * self.page_size
         self.kv_cache = [torch.zeros(slots, c.kv_cache_dim, dtype=self.kv_dtype, device=self.device)
                          for _ in self.layers]
+        if c.index_n_heads:
+            self.ix_cache = [torch.zeros(slots, c.index_head_dim, dtype=self.kv_dtype, device=self.device)
+                             for _ in self.layers]
+            self.ix_scale = [torch.ones(slots, dtype=torch.float32, device=self.device) for _ in self.layers]
         if c.engram_layers:
             self.tok_cache = torch.full((slots,), -1, dtype=torch.int32, device=self.device)
 
     def kv_bytes_per_token(self) -> int:
-        per = self.cfg.kv_cache_dim * torch.tensor([], dtype=self.kv_dtype).element_size()
-        return per * len(self.layers) + (4 if self.cfg.engram_layers else 0)
+        c = self.cfg
+        es = torch.tensor([], dtype=self.kv_dtype).element_size()
+        per = c.kv_cache_dim * es + ((c.index_head_dim * es + 4) if c.index_n_heads else 0)
+        return per * len(self.layers) + (4 if c.engram_layers else 0)
 
     def vocab_offset(self) -> int:
         rows = getattr(self.lm_head, "rows", None)
@@ -131,9 +142,19 @@ class DeepseekV4Model:
         q_lat = ops.rmsnorm_act(qkv[:, :ql], aw.q_norm, c.rms_norm_eps, aw.wq_b, keep_hf=False)
         ops.kv_store_v4(qkv[:, ql:ql + L], aw.kv_norm, c.rms_norm_eps, self.rope_table, fb.positions,
                         self.kv_cache[i], fb.out_slots, self.kv_scale[i], rd)
-        q = aw.wq_b(q_lat, out_dtype=od).view(T, self.heads, L)
+        qo = aw.wq_b(q_lat, out_dtype=od)
+        q = qo[:, : self.heads * L].view(T, self.heads, L)
+        topk = None
+        if c.index_n_heads:
+            nh, hd = c.index_n_heads, c.index_head_dim
+            base = ql + L
+            ops.index_k_store(qkv[:, base: base + hd], aw.ix_k_norm_w, aw.ix_k_norm_b, 1e-6, self.rope_table,
+                              fb.positions, self.ix_cache[i], self.ix_scale[i], fb.out_slots)
+            topk = ops.indexer_topk(qo[:, self.heads * L: self.heads * L + nh * hd], qkv[:, base + hd: base + hd + nh],
+                                    (nh * hd) ** -0.5, self.rope_table, self.ix_cache[i], self.ix_scale[i], fb,
+                                    self.page_size, c.index_topk, c.index_swa)
         o = ops.mqa_attention(q, self.kv_cache[i], self.kv_scale[i], fb, c.softmax_scale, self.page_size, aw.sink,
-                              self.rope_table, rd)
+                              self.rope_table, rd, topk)
         z = ops.absorb_o(o.reshape(T, self.groups, -1), aw.wo_a, quantize=aw.wo_b.quantized)
         y = aw.wo_b(z, out_dtype=od)
         return self._reduce(y)
@@ -268,13 +289,21 @@ def build_model_v4(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState, sd: 
         p = f"model.layers.{i}."
         a = p + "self_attn."
         wq_b = split(get(a + "wq_b.weight").view(H, L, -1), 0, tp, tr).reshape(Hl * L, -1)
+        a_rows, b_rows = [get(a + "wqkv_a.weight")], [wq_b]
+        if cfg.index_n_heads:
+            ix = a + "indexer."
+            a_rows += [get(ix + "wk.weight"), get(ix + "weights_proj.weight")]
+            b_rows += [get(ix + "wq_b.weight")]
         wo_a = split(get(a + "wo_a.weight").view(G, R, -1), 0, tp, tr).to(dev, wdt).contiguous()
         wo_b = split(get(a + "wo_b.weight"), 1, tp, tr)
         sink = split(get(a + "attn_sink"), 0, tp, tr).to(dev).contiguous() if cfg.attn_sink else None
-        aw = V4AttnWeights(wqkv_a=Linear(_quantize(get(a + "wqkv_a.weight"), fmt_d, dev)),
+        aw = V4AttnWeights(wqkv_a=Linear(_quantize(torch.cat(a_rows, 0), fmt_d, dev)),
                            q_norm=get(a + "q_norm.weight").to(dev), kv_norm=get(a + "kv_norm.weight").to(dev),
-                           wq_b=Linear(_quantize(wq_b, fmt_d, dev)), wo_a=wo_a,
+                           wq_b=Linear(_quantize(torch.cat(b_rows, 0), fmt_d, dev)), wo_a=wo_a,
                            wo_b=Linear(_quantize(wo_b, fmt_d, dev)), sink=sink)
+        if cfg.index_n_heads:
+            aw.ix_k_norm_w = get(a + "indexer.k_norm.weight").to(dev)
+            aw.ix_k_norm_b = get(a + "indexer.k_norm.bias").to(dev)
         eng = None
         if i in cfg.engram_layers:
             e = p + "engram."

@@ -83,6 +83,13 @@ def init_weights_v4(cfg: ModelConfig, seed: int = 0, std: float = 0.02) -> Dict[
         sd[a + "wo_b.weight"] = rn(h, G * R)
         if cfg.attn_sink:
             sd[a + "attn_sink"] = rn(H, s=1.0)
+        if cfg.index_n_heads:
+            ix = a + "indexer."
+            sd[ix + "wq_b.weight"] = rn(cfg.index_n_heads * cfg.index_head_dim, cfg.q_lora_rank)
+            sd[ix + "wk.weight"] = rn(cfg.index_head_dim, h)
+            sd[ix + "k_norm.weight"] = torch.ones(cfg.index_head_dim)
+            sd[ix + "k_norm.bias"] = torch.zeros(cfg.index_head_dim)
+            sd[ix + "weights_proj.weight"] = rn(cfg.index_n_heads, h)
         m = p + "mlp."
         if cfg.is_moe_layer(i):
             sd[m + "gate.weight"] = rn(cfg.n_routed_experts, h)
@@ -144,6 +151,7 @@ class ReferenceV4Model:
     def reset(self, batch: int):
         c = self.cfg
         self.cache = [torch.zeros(batch, self.max_len, c.kv_lora_rank) for _ in range(c.num_hidden_layers)]
+        self.ik = [torch.zeros(batch, self.max_len, c.index_head_dim) for _ in range(c.num_hidden_layers)]
         self.tokens = torch.full((batch, self.max_len), -1, dtype=torch.int64)
 
     # -- mHC ------------------------------------------------------------------
@@ -173,7 +181,10 @@ class ReferenceV4Model:
         keys = self.cache[i][:, :end]                                          # [B, end, L]
         s = torch.einsum("bshd,bld->bhsl", q, keys) * c.softmax_scale
         causal = torch.arange(end).view(1, end) <= (start + torch.arange(S)).view(S, 1)
-        s = s.masked_fill(~causal.view(1, 1, S, end), float("-inf"))
+        mask = causal.view(1, 1, S, end)
+        if c.index_n_heads:
+            mask = mask & self._indexer_select(i, x, qr, pos, start, S).unsqueeze(1)
+        s = s.masked_fill(~mask, float("-inf"))
         if c.attn_sink:
             sink = w[a + "attn_sink"].view(1, H, 1, 1).expand(B, H, S, 1)
             p = torch.cat([s, sink], -1).softmax(-1)[..., :-1]
@@ -186,6 +197,35 @@ class ReferenceV4Model:
         wa = w[a + "wo_a.weight"].view(G, R, (H // G) * L)
         z = torch.einsum("bsgk,grk->bsgr", og, wa).reshape(B, S, G * R)
         return z @ w[a + "wo_b.weight"].T
+
+    def _indexer_select(self, i, x, qr, pos, start, S):
+        """Lightning indexer (as the V3.2 oracle) plus the sliding window:
+        top index_topk causal positions by score, the last index_swa always
+        kept.  Returns bool mask [B, S, end]."""
+        import torch.nn.functional as F
+        from .rope import apply_rope_ref
+        c, w = self.cfg, self.w
+        a = f"model.layers.{i}.self_attn.indexer."
+        B = x.shape[0]
+        nh, hd, rd = c.index_n_heads, c.index_head_dim, c.qk_rope_head_dim
+        q = (qr @ w[a + "wq_b.weight"].T).view(B, S, nh, hd)
+        q = torch.cat([apply_rope_ref(q[..., :rd], pos.expand(B, S), self.rope), q[..., rd:]], -1)
+        k = F.layer_norm(x @ w[a + "wk.weight"].T, (hd,), w[a + "k_norm.weight"], w[a + "k_norm.bias"], 1e-6)
+        k = torch.cat([apply_rope_ref(k[..., :rd], pos.expand(B, S), self.rope), k[..., rd:]], -1)
+        end = start + S
+        self.ik[i][:, start:end] = k
+        keys = self.ik[i][:, :end]
+        hw = (x @ w[a + "weights_proj.weight"].T) * (nh ** -0.5) * (hd ** -0.5)
+        sc = (torch.einsum("bshd,bld->bshl", q, keys).relu() * hw.unsqueeze(-1)).sum(2)
+        qpos = (start + torch.arange(S)).view(S, 1)
+        j = torch.arange(end).view(1, end)
+        causal = j <= qpos
+        sc = sc.masked_fill(~causal, float("-inf"))
+        if c.index_swa:
+            sc = sc.masked_fill(causal & (j > qpos - c.index_swa), float("inf"))
+        idx = sc.topk(min(c.index_topk, end), dim=-1).indices
+        sel = torch.zeros(B, S, end, dtype=torch.bool).scatter_(2, idx, True)
+        return sel & causal
 
     # -- ffn ----------------------------------------------------------------------
     def _mlp(self, pre: str, x: torch.Tensor) -> torch.Tensor:

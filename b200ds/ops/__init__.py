@@ -312,18 +312,19 @@ def index_k_store(k, ln_w, ln_b, eps: float, table, pos, cache: torch.Tensor, sc
         scale[slots.long()] = 1.0
 
 
-def indexer_topk(q_raw, w_raw, w_factor: float, table, k_cache, k_scale, fb, page_size: int, topk: int):
+def indexer_topk(q_raw, w_raw, w_factor: float, table, k_cache, k_scale, fb, page_size: int, topk: int,
+                 swa: int = 0):
     """Top-k cache positions [T, topk] (-1 padded, ascending) of the lightning
     indexer: q_raw [T, NH*hd] before RoPE, w_raw [T, NH] head weights before
     the w_factor scaling."""
     if _use_native(q_raw):
-        return _native().indexer_topk(q_raw, w_raw, w_factor, table, k_cache, k_scale, fb, page_size, topk)
+        return _native().indexer_topk(q_raw, w_raw, w_factor, table, k_cache, k_scale, fb, page_size, topk, swa)
     T, nh = w_raw.shape
     rd = table.shape[-1]
     q = to_float(q_raw).reshape(T, nh, -1)
     q = torch.cat([ref_rope(q[..., :rd], fb.positions, table), q[..., rd:]], -1)
     w = to_float(w_raw) * w_factor
-    return ref.indexer_scores(q, w, k_cache, k_scale, fb.block_table, fb.q_seq, fb.positions, page_size, topk)
+    return ref.indexer_scores(q, w, k_cache, k_scale, fb.block_table, fb.q_seq, fb.positions, page_size, topk, swa)
 
 
 def ref_rope(x: torch.Tensor, pos: torch.Tensor, table: torch.Tensor) -> torch.Tensor:

@@ -597,7 +597,7 @@ def ix_splits(T: int, max_len: int) -> int:
 _IX_SCORE_BYTES = 512 << 20      # cap on the fp32 score scratch per call
 
 
-def indexer_topk(q_raw, w_raw, w_factor, table, k_cache, k_scale, fb, page_size, topk):
+def indexer_topk(q_raw, w_raw, w_factor, table, k_cache, k_scale, fb, page_size, topk, swa=0):
     """Indexer: RoPE + e4m3 queries, tcgen05 scores, radix top-k.  Queries are
     processed in slices so the [T, capacity] fp32 score scratch stays bounded."""
     T, nh = w_raw.shape
@@ -617,6 +617,11 @@ def indexer_topk(q_raw, w_raw, w_factor, table, k_cache, k_scale, fb, page_size,
         scores = torch.empty(n, cap, dtype=torch.float32, device=dev)
         _C.ix_score(q8, wq, kc, k_scale, fb.block_table, fb.q_seq[t0:t1], pos, page_size,
                     ix_splits(n, max_len), scores)
+        if swa > 0:
+            # the last `swa` positions up to each query always survive the top-k
+            j = torch.arange(cap, device=dev).unsqueeze(0)
+            p = pos.long().unsqueeze(1)
+            scores.masked_fill_((j > p - swa) & (j <= p), float("inf"))
         _C.topk_select(scores, pos, out[t0:t1])
     return out
 

@@ -123,7 +123,7 @@ def mla_attention(q_abs: torch.Tensor, q_pe: torch.Tensor, kv_cache: torch.Tenso
 
 def indexer_scores(q: torch.Tensor, w: torch.Tensor, k_cache: torch.Tensor, k_scale: torch.Tensor,
                    block_table: torch.Tensor, q_seq: torch.Tensor, q_pos: torch.Tensor,
-                   page_size: int, topk: int) -> torch.Tensor:
+                   page_size: int, topk: int, swa: int = 0) -> torch.Tensor:
     """Lightning indexer top-k: score[s] = sum_h w[t,h] * relu(q[t,h] . k[s]).
 
     q [T, Hi, D] (float), w [T, Hi], k_cache [slots, D] e4m3 with per-token
@@ -139,6 +139,8 @@ def indexer_scores(q: torch.Tensor, w: torch.Tensor, k_cache: torch.Tensor, k_sc
         slots = pages * page_size + pos % page_size
         k = k_cache[slots].float() * k_scale[slots].float().unsqueeze(-1)
         sc = ((q[t].float() @ k.T).relu() * w[t].float().unsqueeze(-1)).sum(0)
+        if swa > 0:
+            sc[max(0, n - swa):] = float("inf")       # the window is always kept
         kk = min(topk, n)
         idx = sc.topk(kk).indices
         out[t, :kk] = idx.sort().values.to(torch.int32)

@@ -132,3 +132,24 @@ def test_v4_tp2_gloo_matches_single():
     eng, cfg = _v4_engine()
     single = [o.token_ids for o in eng.generate(_prompts(cfg).tolist(), SamplingParams(max_tokens=6))]
     assert res[0] == single and res[1] == single
+
+
+def test_v4_sparse_indexer_with_window_matches_oracle():
+    """V4 with the lightning indexer + sliding window selection (top-6 by
+    score, the last 3 positions always kept) over 20+ cached tokens.  8
+    indexer heads: a key scores exactly 0 only when every head's ReLU is 0,
+    and such ties (ordered differently by the oracle's batched top-k) then
+    stay away from the selection boundary."""
+    from b200ds import build_model_from
+    from b200ds.config import EngineConfig, tiny_v4_config
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.reference_v4 import ReferenceV4Model, init_weights_v4
+    cfg = tiny_v4_config(index_n_heads=8, index_head_dim=32, index_topk=6, index_swa=3)
+    sd = init_weights_v4(cfg, 0)
+    ecfg = EngineConfig(page_size=8, cuda_graphs=False, enable_prefix_cache=False, max_prefill_tokens=9)
+    eng = Engine(build_model_from(cfg, ecfg, sd, device="cpu"), ecfg)
+    prompts = _prompts(cfg, 2, 21, seed=7)
+    outs = eng.generate(prompts.tolist(), SamplingParams(max_tokens=5))
+    oracle = ReferenceV4Model(cfg, sd, 128)
+    assert [o.token_ids for o in outs] == oracle.greedy(prompts, 5).tolist()
