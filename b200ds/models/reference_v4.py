@@ -48,7 +48,7 @@ def _e4m3_bytes(x: torch.Tensor) -> torch.Tensor:
 
 def init_weights_v4(cfg: ModelConfig, seed: int = 0, std: float = 0.02) -> Dict[str, torch.Tensor]:
     """Full (unsharded) fp32 state dict of a V4-family model (our parameter
-    names, listed in models/loader_v4.py)."""
+    names, listed in models/deepseek_v4.py::build_model_v4)."""
     assert cfg.is_v4 and cfg.hc_mult > 0
     g = torch.Generator().manual_seed(seed)
 

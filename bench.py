@@ -161,7 +161,7 @@ def main():
         print(json.dumps({"impl": "reference", "unavailable":
                           "the reference is a forward-pass plug-in for an absent SGLang fork (no setup.py/"
                           "pyproject; needs cacheon/dsv41-tp2-upstream, FlashInfer 0.7.1, DeepGEMM, sm_103); "
-                          "pip install of /root/reference fails: 'Directory is not installable'"}))
+                          "pip install of the reference source tree fails: 'Directory is not installable'"}))
         return
     import torch
     import torch.distributed as dist
