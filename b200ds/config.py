@@ -48,6 +48,9 @@ class ModelConfig:
         "beta_fast": 32.0, "beta_slow": 1.0, "mscale": 1.0, "mscale_all_dim": 1.0})
     max_position_embeddings: int = 163840
     tie_word_embeddings: bool = False
+    # multi-token prediction modules after the last layer (DeepSeek-V3 ships 1;
+    # the engine uses the first as the speculative-decoding draft)
+    num_nextn_predict_layers: int = 0
     # Sparse attention (V3.2-style lightning indexer); 0 heads = dense MLA.
     index_n_heads: int = 0
     index_head_dim: int = 128
@@ -308,5 +311,6 @@ class EngineConfig:
     weight_sets: int = 0             # >0: cycle this many distinct layer weight sets (when the model exceeds HBM)
     spec_ngram: int = 0              # >0: speculative decoding with n-gram (prompt lookup) drafts up to this n
     spec_k: int = 4                  # draft tokens verified per step
+    spec_mtp: bool = False           # speculative decoding with the model's MTP module as the draft
     selfcheck: bool = True           # GPU: check each switchable fast path once at start (fail-closed, ranks agree)
     trace: bool = False              # device timestamps per layer phase (also B200_TRACE=1); adds launches

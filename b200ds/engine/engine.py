@@ -58,6 +58,14 @@ class Engine:
             num_pages = ecfg.max_kv_pages or self._auto_pages()
         self.pool = PagePool(num_pages, ecfg.page_size)
         model.allocate_kv(num_pages)
+        self.mtp = getattr(model, "mtp", None) if ecfg.spec_mtp else None
+        if ecfg.spec_mtp:
+            if self.mtp is None:
+                raise ValueError("spec_mtp needs a model with an MTP module (num_nextn_predict_layers > 0)")
+            if ecfg.enable_prefix_cache:
+                # the MTP row of a prefix's last position depends on the token after it
+                raise ValueError("spec_mtp runs without the prefix cache")
+            self.mtp.allocate_kv(num_pages)
         self.radix = RadixCache(self.pool) if ecfg.enable_prefix_cache else None
         self.sched = Scheduler(self.pool, ecfg.max_num_seqs, ecfg.max_prefill_tokens, self.radix)
         self.eos = eos_token_id
@@ -111,7 +119,10 @@ class Engine:
         fb = build_batch(seqs, self.ecfg.page_size, device="cpu")
         fb = self._to_device(fb)
         logits = self.model.forward(fb)
-        return self._sample(step, logits)
+        toks = self._sample(step, logits)
+        if self.mtp is not None and step.kind == "prefill":
+            self._mtp_prefill(step, toks)
+        return toks
 
     def _dp_forward(self, step: Optional[Step]) -> Optional[List[int]]:
         """One lockstep DP-attention forward.  All ranks run the same kind of
@@ -175,7 +186,11 @@ class Engine:
         elif st is None:
             return []
         else:
-            multi = self._spec_decode(st) if (self.ecfg.spec_ngram > 0 and st.kind == "decode") else None
+            multi = None
+            if st.kind == "decode" and self.mtp is not None:
+                multi = self._mtp_decode(st)
+            elif st.kind == "decode" and self.ecfg.spec_ngram > 0:
+                multi = self._spec_decode(st)
             toks = None if multi is not None else self._forward(st)
         if multi is None:
             self.sched.commit(st)
@@ -284,6 +299,113 @@ class Engine:
             out.append(d[:a] + [p[a]])
             self.stats["spec_proposed"] = self.stats.get("spec_proposed", 0) + len(d)
             self.stats["spec_accepted"] = self.stats.get("spec_accepted", 0) + a
+        return out
+
+    # ------------------------------------------------------------------
+    # Speculative decoding with the model's MTP module as the draft
+    def _mtp_run(self, rows, prev_h):
+        """One MTP forward over `rows` (see models/mtp.py::mtp_batch);
+        returns (greedy draft token, MTP hidden) of each request's last row."""
+        from ..models.mtp import mtp_batch
+        fb = mtp_batch(rows, self.ecfg.page_size, "cpu")
+        fb = self._to_device(fb)
+        logits, hid = self.mtp.forward(fb, prev_h)
+        return logits.argmax(-1).tolist(), hid
+
+    def _mtp_chain(self, reqs, first, hid, n_next) -> None:
+        """Drafts 2..spec_k: the module applied to its own hidden state.
+        reqs[i]'s newest draft sits at token position n_next[i]."""
+        drafts = [[t] for t in first]
+        for _ in range(self.ecfg.spec_k - 1):
+            rows = []
+            for r, d, n in zip(reqs, drafts, n_next):
+                j = n + len(d) - 1            # token position of the newest draft
+                if not self.sched._ensure_pages(r, j):
+                    return self._mtp_store(reqs, drafts, hid)
+                rows.append({"tokens": [d[-1]], "j0": j, "pages": r.pages})
+            nxt, hid = self._mtp_run(rows, hid)
+            for d, t in zip(drafts, nxt):
+                d.append(t)
+        self._mtp_store(reqs, drafts, hid)
+
+    @staticmethod
+    def _mtp_store(reqs, drafts, hid) -> None:
+        for r, d in zip(reqs, drafts):
+            r.mtp_drafts = d
+
+    def _mtp_prefill(self, st: Step, toks: List[int]) -> None:
+        """After a prefill chunk: MTP rows for the chunk's positions (and, when
+        the prompt is done, the sampled token's), from the main model's
+        hidden states; finished prompts get their first drafts."""
+        H = self.model.last_residual
+        rows, prev, fin, fin_pos = [], [], [], []
+        off = 0
+        for i, (r, ch, s) in enumerate(zip(st.reqs, st.chunks, st.starts)):
+            n = len(ch)
+            Hr = H[off: off + n]
+            off += n
+            toks_j, prev_j = [], []
+            j0 = max(s, 1)
+            for j in range(j0, s + n):
+                toks_j.append(ch[j - s])
+                prev_j.append(Hr[j - 1 - s] if j - 1 >= s else getattr(r, "mtp_h_prev", None))
+            if st.sample[i]:
+                if not toks_j:
+                    j0 = s + n
+                toks_j.append(toks[i])
+                prev_j.append(Hr[n - 1])
+            r.mtp_h_prev = Hr[n - 1].clone()
+            if toks_j and all(p is not None for p in prev_j):
+                rows.append({"tokens": toks_j, "j0": j0, "pages": r.pages, "req": r, "fin": st.sample[i]})
+                prev.extend(prev_j)
+        if not rows:
+            return
+        draft, hid = self._mtp_run(rows, torch.stack(prev))
+        reqs = [row["req"] for row in rows if row["fin"]]
+        if not reqs:
+            return
+        idx = [k for k, row in enumerate(rows) if row["fin"]]
+        n_next = [row["j0"] + len(row["tokens"]) for row in rows if row["fin"]]
+        self._mtp_chain(reqs, [draft[k] for k in idx], hid[idx], n_next)
+
+    def _mtp_decode(self, st: Step) -> Optional[List[List[int]]]:
+        """Verify the MTP drafts (greedy) in one main-model forward with logits
+        and hidden states at every row, then run the MTP module over the
+        accepted tokens for the next drafts."""
+        if any(r.params.temperature > 0 for r in st.reqs):
+            for r in st.reqs:
+                r.mtp_drafts = []
+            return None
+        drafts = []
+        for r in st.reqs:
+            room = r.params.max_tokens - len(r.output) - 1
+            d = list(getattr(r, "mtp_drafts", []))[: max(0, room)]
+            if d and not self.sched._ensure_pages(r, r.cached + 1 + len(d)):
+                d = []
+            drafts.append(d)
+        seqs = [{"tokens": ch + d, "start": s, "pages": r.pages}
+                for r, ch, s, d in zip(st.reqs, st.chunks, st.starts, drafts)]
+        fb = build_batch(seqs, self.ecfg.page_size, device="cpu")
+        fb.last_idx = torch.arange(fb.num_tokens, dtype=torch.int64)     # logits at every position
+        fb = self._to_device(fb)
+        pred = self.model.forward(fb).argmax(-1).tolist()
+        H = self.model.last_residual
+        starts, off = [], 0
+        for d in drafts:
+            starts.append(off)
+            off += 1 + len(d)
+        out = self._accept(st, drafts, pred, starts)
+        rows, prev = [], []
+        for r, o, s0, n in zip(st.reqs, out, starts, st.starts):
+            # token positions n + 1 .. n + len(o) hold the accepted tokens
+            rows.append({"tokens": o, "j0": n + 1, "pages": r.pages})
+            prev.extend(H[s0 + k] for k in range(len(o)))
+            r.mtp_h_prev = H[s0 + len(o) - 1].clone()
+        if not all(self.sched._ensure_pages(r, n + len(o)) for r, o, n in zip(st.reqs, out, st.starts)):
+            self._mtp_store(st.reqs, [[] for _ in st.reqs], None)
+            return out
+        draft, hid = self._mtp_run(rows, torch.stack(prev))
+        self._mtp_chain(st.reqs, draft, hid, [n + len(o) + 1 for o, n in zip(out, st.starts)])
         return out
 
     def _check_device_errors(self) -> None:

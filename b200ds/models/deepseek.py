@@ -293,18 +293,22 @@ class DeepseekModel:
         return out
 
     @torch.no_grad()
-    def forward(self, fb: ForwardBatch) -> torch.Tensor:
+    def forward(self, fb: ForwardBatch, x0: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Returns logits [B, V] (full vocab) for each sequence's last token."""
-        h = self._hidden(fb)
+        h = self._hidden(fb, x0)
         return ops.lm_head_logits(self._last_hidden(h, fb), self.lm_head, self.ps)
 
-    def _hidden(self, fb: ForwardBatch):
-        """All decoder layers + the final norm; returns the normed hidden."""
+    def _hidden(self, fb: ForwardBatch, x0: Optional[torch.Tensor] = None):
+        """All decoder layers + the final norm; returns the normed hidden.
+        x0: the initial residual stream instead of the token embeddings (the
+        MTP module).  The pre-norm final residual of every row is kept in
+        `last_residual` (the speculative draft's input)."""
         c = self.cfg
         tr = self.tracer
         tr.reset()
         tr.mark("embed")
-        residual = self.embed[fb.input_ids.long()].float()      # fp32 residual stream
+        residual = (self.embed[fb.input_ids.long()].float() if x0 is None
+                    else x0.float().contiguous())                  # fp32 residual stream
         h = ops.rmsnorm_act(residual, self.layers[0].in_ln, c.rms_norm_eps, self.layers[0].attn.qkv_a)
         for i, lw in enumerate(self.layers):
             tr.mark(f"L{i}.attn")
@@ -321,6 +325,7 @@ class DeepseekModel:
                 f, residual, nxt.in_ln if nxt else self.final_ln, c.rms_norm_eps, ps_f,
                 "ffn", nxt.attn.qkv_a if nxt else None)
         tr.mark("head")
+        self.last_residual = residual
         return h
 
     def _last_hidden(self, h, fb: ForwardBatch) -> torch.Tensor:

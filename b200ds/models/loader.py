@@ -127,8 +127,7 @@ def build_model(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState,
         return t.chunk(n, dim)[r].contiguous() if n > 1 else t
 
     fmt_d = cfg.dense_format
-    layers: List[LayerWeights] = []
-    for i in range(cfg.num_hidden_layers):
+    def layer_at(i: int) -> LayerWeights:
         p = f"model.layers.{i}."
         a = p + "self_attn."
         qa = get(a + "q_a_proj.weight")
@@ -157,9 +156,10 @@ def build_model(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState,
             aw.ix_k_norm_w = sd[ix + "k_norm.weight"].float().to(dev)
             aw.ix_k_norm_b = sd[ix + "k_norm.bias"].float().to(dev)
         ffn = build_ffn(cfg, sd, get, split, p + "mlp.", i, ps, dev)
-        layers.append(LayerWeights(in_ln=sd[p + "input_layernorm.weight"].float().to(dev),
-                                   post_ln=sd[p + "post_attention_layernorm.weight"].float().to(dev),
-                                   attn=aw, ffn=ffn))
+        return LayerWeights(in_ln=sd[p + "input_layernorm.weight"].float().to(dev),
+                            post_ln=sd[p + "post_attention_layernorm.weight"].float().to(dev), attn=aw, ffn=ffn)
+
+    layers: List[LayerWeights] = [layer_at(i) for i in range(cfg.num_hidden_layers)]
     emb_dt = torch.bfloat16 if dev.type == "cuda" else torch.float32
     embed = sd["model.embed_tokens.weight"].float().to(dev, emb_dt)
     head_full = sd["model.embed_tokens.weight"] if cfg.tie_word_embeddings else sd["lm_head.weight"]
@@ -168,8 +168,17 @@ def build_model(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState,
     head = _quantize(head, "mxfp8", dev) if fmt_d == "mxfp8" and dev.type == "cuda" else head.to(dev, emb_dt)
     if kv_dtype is None:
         kv_dtype = torch.float8_e4m3fn if dev.type == "cuda" else torch.float32
-    return DeepseekModel(cfg, ecfg, ps, layers, embed, sd["model.norm.weight"].float().to(dev), head, dev,
-                         kv_dtype=kv_dtype)
+    model = DeepseekModel(cfg, ecfg, ps, layers, embed, sd["model.norm.weight"].float().to(dev), head, dev,
+                          kv_dtype=kv_dtype)
+    L = cfg.num_hidden_layers
+    m = f"model.layers.{L}."
+    if cfg.num_nextn_predict_layers and (m + "eh_proj.weight") in sd:
+        from .mtp import MTPDraft
+        block = DeepseekModel(cfg, ecfg, ps, [layer_at(L)], embed, sd[m + "shared_head.norm.weight"].float().to(dev),
+                              head, dev, kv_dtype=kv_dtype)
+        model.mtp = MTPDraft(block, sd[m + "enorm.weight"].float().to(dev), sd[m + "hnorm.weight"].float().to(dev),
+                             Linear(_quantize(get(m + "eh_proj.weight"), fmt_d, dev)))
+    return model
 
 
 # ---------------------------------------------------------------------------

@@ -16,6 +16,7 @@ sqrtsoftplus.
 """
 from __future__ import annotations
 
+import dataclasses
 import math
 from typing import Dict, List, Optional
 
@@ -85,6 +86,21 @@ def init_weights(cfg: ModelConfig, seed: int = 0, std: float = 0.02,
     sd["model.norm.weight"] = torch.ones(h, dtype=dtype)
     if not cfg.tie_word_embeddings:
         sd["lm_head.weight"] = rn(cfg.vocab_size, h)
+    if cfg.num_nextn_predict_layers:
+        # MTP module (HF layout: one extra decoder layer after the last, with
+        # embedding / hidden norms, the [2h -> h] input projection and a head norm)
+        L = cfg.num_hidden_layers
+        src = init_weights(dataclasses.replace(cfg, num_hidden_layers=L + 1, num_nextn_predict_layers=0,
+                                               first_k_dense_replace=min(cfg.first_k_dense_replace, L)),
+                           seed + 1, std, dtype)
+        m = f"model.layers.{L}."
+        for k, v in src.items():
+            if k.startswith(m):
+                sd[k] = v
+        sd[m + "enorm.weight"] = torch.ones(h, dtype=dtype)
+        sd[m + "hnorm.weight"] = torch.ones(h, dtype=dtype)
+        sd[m + "eh_proj.weight"] = rn(h, 2 * h)
+        sd[m + "shared_head.norm.weight"] = torch.ones(h, dtype=dtype)
     return sd
 
 

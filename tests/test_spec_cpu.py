@@ -55,3 +55,66 @@ def test_verify_batch_layout_matches_unpadded():
     got = m.forward(vb)
     assert got.shape[0] == 15
     assert torch.allclose(got[[0, 1, 2, 5]], want, atol=1e-5)
+
+
+def test_mtp_speculative_decoding_matches_greedy():
+    """MTP drafts (DeepSeek-V3's next-token module as the draft, chained
+    for spec_k tokens) verified greedily: the same tokens as plain greedy
+    decoding, under chunked prefill; drafts are proposed every step."""
+    from b200ds import build_model_from
+    from b200ds.config import EngineConfig, tiny_config
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.reference import init_weights
+    import torch
+    cfg = tiny_config(num_nextn_predict_layers=1)
+    sd = init_weights(cfg, 0)
+    g = torch.Generator().manual_seed(3)
+    prompts = torch.randint(0, cfg.vocab_size, (3, 13), generator=g).tolist()
+
+    def run(**kw):
+        ecfg = EngineConfig(page_size=8, cuda_graphs=False, enable_prefix_cache=False, max_prefill_tokens=7, **kw)
+        eng = Engine(build_model_from(cfg, ecfg, sd, device="cpu"), ecfg)
+        outs = eng.generate(prompts, SamplingParams(max_tokens=10))
+        return [o.token_ids for o in outs], eng.stats
+    base, _ = run()
+    spec, stats = run(spec_mtp=True, spec_k=3)
+    assert spec == base
+    assert stats.get("spec_proposed", 0) > 0
+
+
+def test_mtp_first_draft_matches_one_shot_computation():
+    """The first draft after a chunked prefill equals the MTP module run in
+    one pass over z_j = eh_proj[rms(Emb(x_j)); rms(h_{j-1})], j = 1..P
+    (x_P = the sampled token), at MTP positions 0..P-1."""
+    import torch
+    from b200ds import build_model_from
+    from b200ds.config import EngineConfig, tiny_config
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.batch import build_batch
+    from b200ds.models.reference import init_weights
+    cfg = tiny_config(num_nextn_predict_layers=1)
+    sd = init_weights(cfg, 0)
+    prompt = torch.randint(0, cfg.vocab_size, (11,), generator=torch.Generator().manual_seed(5)).tolist()
+    ecfg = EngineConfig(page_size=8, cuda_graphs=False, enable_prefix_cache=False, max_prefill_tokens=4,
+                        spec_mtp=True, spec_k=1)
+    eng = Engine(build_model_from(cfg, ecfg, sd, device="cpu"), ecfg)
+    r = eng.add_request(prompt, SamplingParams(max_tokens=4))
+    while r.t_first is None:
+        eng.step()
+    x_new, draft = r.output[0], r.mtp_drafts[0]
+    # one-shot: main model hiddens over the whole prompt, then the MTP block
+    ref_eng = Engine(build_model_from(cfg, EngineConfig(page_size=8, cuda_graphs=False,
+                                                        enable_prefix_cache=False), sd, device="cpu"),
+                     EngineConfig(page_size=8, cuda_graphs=False, enable_prefix_cache=False))
+    m = ref_eng.model
+    pages = ref_eng.pool.alloc(2)
+    m.forward(build_batch([{"tokens": prompt, "start": 0, "pages": pages}], 8))
+    H = m.last_residual
+    mtp = m.mtp
+    mtp.allocate_kv(16)
+    toks = prompt[1:] + [x_new]
+    fb = build_batch([{"tokens": toks, "start": 0, "pages": pages}], 8)
+    logits, _ = mtp.forward(fb, H)
+    assert int(logits.argmax(-1)[0]) == draft
