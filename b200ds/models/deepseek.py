@@ -118,6 +118,8 @@ class DeepseekModel:
         self.page_size = ecfg.page_size
         from ..utils.trace import null_tracer
         self.tracer = null_tracer()       # the engine installs a Tracer when tracing is on
+        self.mtp = None                   # MTP draft module (models/mtp.py), attached by the loader
+        self.last_residual = None
         if self.device.type == "cuda":
             for lw in layers:       # [H, L, nope] copy of W_uk for the tensor-core absorption
                 w = lw.attn.w_uk

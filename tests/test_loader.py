@@ -50,3 +50,24 @@ def test_fp8_checkpoint_roundtrip(tmp_path):
     # close to the fp32 oracle, not equal
     rel = ((logs[0] - ologits[0]).norm() / ologits[0].norm()).item()
     assert rel < 0.25, rel
+
+
+def test_mtp_layer_from_checkpoint(tmp_path):
+    """A checkpoint with DeepSeek-V3's MTP layer (layer num_hidden_layers:
+    enorm / hnorm / eh_proj / decoder layer / shared_head.norm, fp8 blocks)
+    loads as the speculative draft; MTP decoding gives the greedy tokens."""
+    from b200ds import EngineConfig, SamplingParams, load_engine
+    from b200ds.config import ModelConfig, tiny_config
+    from b200ds.models.loader import save_checkpoint_fp8
+    from b200ds.models.reference import init_weights
+    cfg = tiny_config(dense_format="mxfp8", expert_format="mxfp8", num_nextn_predict_layers=1)
+    save_checkpoint_fp8(init_weights(cfg, 0), str(tmp_path), cfg)
+    assert ModelConfig.from_hf(str(tmp_path / "config.json")).num_nextn_predict_layers == 1
+    prompts = torch.randint(0, cfg.vocab_size, (2, 12), generator=torch.Generator().manual_seed(2)).tolist()
+    outs = {}
+    for mtp in (False, True):
+        ecfg = EngineConfig(page_size=8, cuda_graphs=False, enable_prefix_cache=False, spec_mtp=mtp, spec_k=2)
+        eng = load_engine(cfg, weights=str(tmp_path), ecfg=ecfg, device="cpu")
+        assert eng.model.mtp is not None
+        outs[mtp] = [o.token_ids for o in eng.generate(prompts, SamplingParams(max_tokens=6))]
+    assert outs[True] == outs[False]
