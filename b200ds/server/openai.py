@@ -89,6 +89,8 @@ class EngineWorker:
                     loop.call_soon_threadsafe(q.put_nowait, ("done", r.finish_reason))
                     self.metrics.finish(r)
                     del self.subs[rid]
+        if self.ps is not None and self.ps.world_size > 1:
+            _broadcast_requests(self.ps, None)      # followers stop
 
 
 def _broadcast_requests(ps, reqs):
@@ -98,10 +100,99 @@ def _broadcast_requests(ps, reqs):
     return obj[0]
 
 
+class DPEngineWorker(EngineWorker):
+    """DP attention serving: rank 0 takes the HTTP requests and assigns each
+    to a rank round-robin; every rank serves its own requests and all ranks
+    step in lockstep (the engine agrees on each step's shape); each step the
+    ranks' new tokens are gathered to rank 0, which streams them out.
+    Stopping broadcasts a sentinel that ends the followers' loops."""
+
+    def __init__(self, engine, tokenizer, ps):
+        super().__init__(engine, tokenizer, ps)
+        self.next_gid = 0
+        self.own: Dict[int, list] = {}      # gid -> [request, tokens sent]
+
+    def _run(self):
+        eng, ps = self.engine, self.ps
+        world = ps.world_size
+        while not self._stop.is_set():
+            new = self._admit()
+            batch = []
+            for prompt, params, loop, q in new:
+                gid = self.next_gid
+                self.next_gid += 1
+                self.subs[gid] = (loop, q, 0, None)
+                self.metrics.requests += 1
+                batch.append((prompt, params.__dict__, gid % world, gid))
+            _broadcast_requests(ps, batch)
+            _dp_admit(eng, ps, batch, self.own)
+            t0 = time.perf_counter()
+            eng.step()
+            if eng.sched.has_work:
+                self.metrics.step_time.append(time.perf_counter() - t0)
+            for upd in _dp_gather(ps, _dp_updates(self.own)):
+                for gid, toks, fin, reason, r in upd:
+                    loop, q, sent, _ = self.subs[gid]
+                    if toks:
+                        loop.call_soon_threadsafe(q.put_nowait, ("tokens", toks))
+                    if fin:
+                        loop.call_soon_threadsafe(q.put_nowait, ("done", reason))
+                        if r is not None:
+                            self.metrics.finish(r)
+                        del self.subs[gid]
+            if not new and not self.subs:
+                time.sleep(0.002)
+        _broadcast_requests(ps, None)           # followers stop
+
+
+def _dp_admit(eng, ps, batch, own) -> None:
+    for prompt, spd, owner, gid in batch:
+        if owner == ps.rank:
+            own[gid] = [eng.add_request(prompt, SamplingParams(**spd)), 0]
+
+
+def _dp_updates(own) -> list:
+    out = []
+    for gid, st in list(own.items()):
+        r, sent = st
+        toks = r.output[sent:]
+        st[1] = len(r.output)
+        if toks or r.finished:
+            out.append((gid, list(toks), r.finished, r.finish_reason, None))
+        if r.finished:
+            del own[gid]
+    return out
+
+
+def _dp_gather(ps, updates) -> list:
+    import torch.distributed as dist
+    objs = [None] * ps.world_size if ps.rank == 0 else None
+    dist.gather_object(updates, objs, dst=0, group=ps.cpu_group)
+    return objs if ps.rank == 0 else []
+
+
+def dp_follower_loop(engine, ps) -> None:
+    """DP ranks > 0: serve the requests assigned to this rank, step in
+    lockstep with rank 0 and send it this rank's new tokens every step."""
+    own: Dict[int, list] = {}
+    while True:
+        batch = _broadcast_requests(ps, [])
+        if batch is None:
+            return
+        _dp_admit(engine, ps, batch, own)
+        engine.step()
+        _dp_gather(ps, _dp_updates(own))
+
+
 def follower_loop(engine, ps) -> None:
-    """Ranks > 0: mirror rank 0's admissions and step in lockstep."""
+    """Ranks > 0: mirror rank 0's admissions and step in lockstep (TP); DP
+    attention engines serve their own share (dp_follower_loop)."""
+    if getattr(engine, "dp", False):
+        return dp_follower_loop(engine, ps)
     while True:
         reqs = _broadcast_requests(ps, None)
+        if reqs is None:
+            return
         for prompt, spd in reqs:
             engine.add_request(prompt, SamplingParams(**spd))
         if engine.sched.has_work:
@@ -260,15 +351,25 @@ def main(argv=None):
     ap.add_argument("--port", type=int, default=8000)
     ap.add_argument("--max-num-seqs", type=int, default=256)
     ap.add_argument("--no-cuda-graphs", action="store_true")
+    ap.add_argument("--dp-attention", action="store_true", help="DP attention + EP experts over all ranks")
+    ap.add_argument("--max-model-len", type=int, default=16384)
+    ap.add_argument("--no-prefix-cache", action="store_true")
+    ap.add_argument("--spec-ngram", type=int, default=0, help="n-gram speculative decoding (max n)")
+    ap.add_argument("--spec-mtp", action="store_true", help="speculative decoding with the model's MTP module")
+    ap.add_argument("--spec-k", type=int, default=4, help="draft tokens verified per step")
+    ap.add_argument("--trace", action="store_true", help="device timestamps per layer phase")
     args = ap.parse_args(argv)
     import uvicorn
     from .. import load_engine
     from ..config import EngineConfig
     from ..engine.tokenizer import load_tokenizer
     from ..parallel.state import init_parallel
-    ps = init_parallel()
-    ecfg = EngineConfig(tp_size=ps.tp_size, ep_size=ps.ep_size, max_num_seqs=args.max_num_seqs,
-                        cuda_graphs=not args.no_cuda_graphs)
+    ps = init_parallel(dp_attention=args.dp_attention)
+    ecfg = EngineConfig(tp_size=1 if args.dp_attention else ps.tp_size, ep_size=ps.ep_size,
+                        dp_attention=args.dp_attention, max_num_seqs=args.max_num_seqs,
+                        cuda_graphs=not args.no_cuda_graphs, max_model_len=args.max_model_len,
+                        enable_prefix_cache=not (args.no_prefix_cache or args.spec_mtp),
+                        spec_ngram=args.spec_ngram, spec_mtp=args.spec_mtp, spec_k=args.spec_k, trace=args.trace)
     eng = load_engine(args.model, weights=args.weights, ecfg=ecfg)
     tok = load_tokenizer(args.model)
     eng.tokenizer = tok
@@ -276,7 +377,7 @@ def main(argv=None):
     if ps.rank != 0:
         follower_loop(eng, ps)
         return
-    worker = EngineWorker(eng, tok, ps).start()
+    worker = (DPEngineWorker(eng, tok, ps) if eng.dp else EngineWorker(eng, tok, ps)).start()
     uvicorn.run(create_app(worker, model_name=str(args.model)), host=args.host, port=args.port, log_level="warning")
 
 
