@@ -303,6 +303,7 @@ class EngineConfig:
     kv_cache_fraction: float = 0.85  # of free HBM after weights
     max_kv_pages: Optional[int] = None
     cuda_graphs: bool = True         # capture decode per batch bucket
+    extend_graphs: bool = False      # also replay prefill chunks up to 2048 tokens from per-bucket graphs
     graph_batch_sizes: tuple = (1, 2, 4, 8, 16, 32, 64, 128, 256)
     enable_prefix_cache: bool = True
     comm_impl: str = "fused"         # "fused" (own NVLink kernels) or "nccl" (baseline)

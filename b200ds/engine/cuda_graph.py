@@ -275,3 +275,105 @@ class VerifyGraphRunner:
     def release(self) -> None:
         self.graphs.clear()
         self.pool = None
+
+
+def build_extend_batch(seqs: List[dict], tokens: int, rows: int, page_size: int, max_pages: int) -> ForwardBatch:
+    """Prefill (extend) batch in a fixed shape: `tokens` token rows and
+    `rows` sequence rows.  Sequence i's new tokens are consecutive; the
+    remaining token rows are padding that belongs to the last sequence row
+    (kept free: rows > len(seqs)), sits at position 0 on reserved page 0 and
+    writes its latent to the scratch slot 0.  last_idx[i] is sequence i's last
+    token (padding rows point at the last token row).  Host tensors."""
+    if len(seqs) >= rows:
+        raise ValueError("extend graphs keep one sequence row for padding")
+    ids = torch.zeros(tokens, dtype=torch.int32)
+    pos = torch.zeros(tokens, dtype=torch.int32)
+    qs = torch.full((tokens,), rows - 1, dtype=torch.int32)
+    slots = torch.zeros(tokens, dtype=torch.int64)
+    lens = torch.ones(rows, dtype=torch.int32)
+    bt = torch.zeros(rows, max_pages, dtype=torch.int32)
+    last = torch.full((rows,), tokens - 1, dtype=torch.int64)
+    t = 0
+    for i, s in enumerate(seqs):
+        toks, st, pages = s["tokens"], s["start"], s["pages"]
+        if len(pages) > max_pages:
+            raise ValueError("sequence longer than EngineConfig.max_model_len")
+        for j, x in enumerate(toks):
+            p = st + j
+            ids[t], pos[t], qs[t] = x, p, i
+            slots[t] = pages[p // page_size] * page_size + p % page_size
+            t += 1
+        if t > tokens:
+            raise ValueError("extend batch larger than its bucket")
+        lens[i] = st + len(toks)
+        last[i] = t - 1
+        bt[i, : len(pages)] = torch.tensor(pages, dtype=torch.int32)
+    return ForwardBatch(input_ids=ids, positions=pos, q_seq=qs, out_slots=slots, seq_lens=lens, block_table=bt,
+                        last_idx=last, is_decode=False, max_q_len=tokens, max_seq_len=max_pages * page_size)
+
+
+class ExtendGraphRunner:
+    """CUDA graphs of prefill forwards in fixed (token, sequence) buckets:
+    every kernel of the step launches from one graph replay instead of the
+    host (the chunks of short prompts are launch-bound).  Logits of each
+    sequence's last token come back for sampling."""
+
+    TOKEN_BUCKETS = (64, 128, 256, 512, 1024, 2048)
+
+    def __init__(self, engine, max_pages: int):
+        self.eng = engine
+        self.model = engine.model
+        self.dev = engine.device
+        ecfg = engine.ecfg
+        self.page_size = ecfg.page_size
+        self.row_buckets = sorted({b + 1 for b in ecfg.graph_batch_sizes if b <= ecfg.max_num_seqs}
+                                  | {ecfg.max_num_seqs + 1})
+        self.max_pages = max_pages
+        self.graphs: Dict[tuple, _Graph] = {}
+        self.pool = None
+
+    def bucket(self, ntok: int, nseq: int):
+        tb = next((b for b in self.TOKEN_BUCKETS if b >= ntok), None)
+        rb = next((b for b in self.row_buckets if b > nseq), None)
+        return None if tb is None or rb is None else (tb, rb)
+
+    def _capture(self, key) -> _Graph:
+        tb, rb = key
+        g = _Graph()
+        host = build_extend_batch([], tb, rb, self.page_size, self.max_pages)
+        g.h = ForwardBatch(**{k: (v.pin_memory() if isinstance(v, torch.Tensor) else v)
+                              for k, v in host.__dict__.items()})
+        g.fb = ForwardBatch(**{k: (v.to(self.dev) if isinstance(v, torch.Tensor) else v)
+                               for k, v in host.__dict__.items()})
+        s = torch.cuda.Stream(device=self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self.model.forward(g.fb)
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        torch.cuda.synchronize(self.dev)
+        g.graph = torch.cuda.CUDAGraph()
+        if self.pool is None:
+            self.pool = torch.cuda.graph_pool_handle()
+        with torch.cuda.graph(g.graph, pool=self.pool):
+            g.logits = self.model.forward(g.fb)
+        self.graphs[key] = g
+        return g
+
+    def run(self, seqs: List[dict]) -> Optional[torch.Tensor]:
+        """Logits [len(seqs), V] of each sequence's last token, or None when
+        the step does not fit a bucket."""
+        key = self.bucket(sum(len(s["tokens"]) for s in seqs), len(seqs))
+        if key is None:
+            return None
+        g = self.graphs.get(key) or self._capture(key)
+        host = build_extend_batch(seqs, key[0], key[1], self.page_size, self.max_pages)
+        for name in ("input_ids", "positions", "q_seq", "out_slots", "seq_lens", "block_table", "last_idx"):
+            getattr(g.h, name).copy_(getattr(host, name))
+            getattr(g.fb, name).copy_(getattr(g.h, name), non_blocking=True)
+        g.graph.replay()
+        return g.logits[: len(seqs)]
+
+    def release(self) -> None:
+        self.graphs.clear()
+        self.pool = None

@@ -73,6 +73,7 @@ class Engine:
         self._next_rid = 0
         self.graphs = None
         self.verify_graphs, self.verify_graphs_ok = None, True
+        self.extend_graphs, self.extend_graphs_ok = None, True
         if self.device.type == "cuda" and ecfg.cuda_graphs:
             from .cuda_graph import DecodeGraphRunner
             self.graphs = DecodeGraphRunner(self)
@@ -116,6 +117,21 @@ class Engine:
                 for r, ch, st in zip(step.reqs, step.chunks, step.starts)]
         if step.kind == "decode" and self.graphs is not None and self.graphs.can_run(len(seqs)):
             return self.graphs.run(step, seqs)
+        if (step.kind == "prefill" and self.graphs is not None and self.ecfg.extend_graphs and self.mtp is None
+                and self.extend_graphs_ok):
+            if self.extend_graphs is None:
+                from .cuda_graph import ExtendGraphRunner
+                self.extend_graphs = ExtendGraphRunner(self, self.graphs.max_pages)
+            try:
+                logits = self.extend_graphs.run(seqs)
+            except RuntimeError as e:      # capture failed: eager prefill from now on
+                from ..utils import levers
+                levers.announce("extend-graphs-off", f"extend graphs off ({e}); eager prefill")
+                self.extend_graphs.release()
+                self.extend_graphs, self.extend_graphs_ok = None, False
+                logits = None
+            if logits is not None:
+                return self._sample(step, logits)
         fb = build_batch(seqs, self.ecfg.page_size, device="cpu")
         fb = self._to_device(fb)
         logits = self.model.forward(fb)

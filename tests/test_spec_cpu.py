@@ -118,3 +118,24 @@ def test_mtp_first_draft_matches_one_shot_computation():
     fb = build_batch([{"tokens": toks, "start": 0, "pages": pages}], 8)
     logits, _ = mtp.forward(fb, H)
     assert int(logits.argmax(-1)[0]) == draft
+
+
+def test_extend_batch_layout_matches_ragged():
+    """Fixed-shape prefill layout (token bucket with padding on a spare
+    sequence row, scratch slot, page 0) gives the ragged batch's last-token
+    logits."""
+    import torch
+    from b200ds import build_model_from
+    from b200ds.config import EngineConfig, tiny_config
+    from b200ds.engine.cuda_graph import build_extend_batch
+    from b200ds.models.batch import build_batch
+    from b200ds.models.reference import init_weights
+    cfg = tiny_config()
+    m = build_model_from(cfg, EngineConfig(page_size=8, cuda_graphs=False), init_weights(cfg, 0), device="cpu")
+    m.allocate_kv(16)
+    g = torch.Generator().manual_seed(4)
+    a, b = torch.randint(0, 1000, (11,), generator=g).tolist(), torch.randint(0, 1000, (6,), generator=g).tolist()
+    seqs = [{"tokens": a, "start": 0, "pages": [1, 2]}, {"tokens": b, "start": 0, "pages": [3]}]
+    want = m.forward(build_batch(seqs, 8))
+    got = m.forward(build_extend_batch(seqs, 32, 4, 8, 4))
+    assert got.shape[0] == 4 and torch.allclose(got[:2], want, atol=1e-5)
