@@ -39,7 +39,7 @@ from ..config import EngineConfig, ModelConfig
 from ..ops import EngramWeights, HcWeights
 from ..parallel.state import ParallelState
 from .batch import ForwardBatch
-from .deepseek import DeepseekModel, DenseWeights, Linear, MoEWeights
+from .deepseek import DenseWeights, Linear, MoEWeights
 from .rope import cos_sin_table
 
 
@@ -165,20 +165,11 @@ class DeepseekV4Model:
         if isinstance(lw.ffn, DenseWeights):
             return self._reduce(lw.ffn.down(ops.gate_up_swiglu(h, lw.ffn.gate_up), out_dtype=od))
         mw: MoEWeights = lw.ffn
-        side = self.device.type == "cuda" and ops.get_impl() == "native" and mw.shared_gate_up is not None
-        shared = None
-        if side:
-            # the shared expert is independent of routing: a parallel branch
-            # on the side stream (also inside the captured decode graph)
-            shared = DeepseekModel._fork(self, lambda: mw.shared_down(ops.gate_up_swiglu(h, mw.shared_gate_up),
-                                                                      out_dtype=od), h)
         w, ids = ops.router(h, mw.gate, mw.bias, c)
         if fb.is_decode and c.prune_budget > 0:
             w, ids = ops.e5_prune(w, ids, c, c.n_routed_experts)
         out = ops.moe_experts(h, w, ids, mw.experts, out_dtype=od, n_experts_total=c.n_routed_experts)
-        if side:
-            out = out + DeepseekModel._join(self, shared)
-        elif mw.shared_gate_up is not None:
+        if mw.shared_gate_up is not None:
             out = out + mw.shared_down(ops.gate_up_swiglu(h, mw.shared_gate_up), out_dtype=od)
         return self._reduce(out.to(od))
 
