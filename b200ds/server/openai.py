@@ -218,7 +218,7 @@ class _Metrics:
         if r.t_done is not None and len(r.output) > 1:
             self.tpot.append((r.t_done - r.t_first) / (len(r.output) - 1))
 
-    def prometheus(self) -> str:
+    def prometheus(self, engine_stats=None, switches=None) -> str:
         def q(xs, p):
             if not xs:
                 return 0.0
@@ -235,6 +235,12 @@ class _Metrics:
             f'b200ds_tpot_seconds{{quantile="0.99"}} {q(self.tpot, 0.99)}',
             f'b200ds_step_seconds{{quantile="0.5"}} {q(self.step_time[-1000:], 0.5)}',
         ]
+        st = engine_stats or {}
+        for k in ("steps", "prefill_tokens", "decode_tokens", "spec_proposed", "spec_accepted"):
+            if k in st:
+                lines.append(f"b200ds_engine_{k}_total {int(st[k])}")
+        for k, v in sorted((switches or {}).items()):
+            lines.append(f'b200ds_switch{{name="{k}"}} {int(bool(v))}')
         return "\n".join(lines) + "\n"
 
 
@@ -338,7 +344,8 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
 
     @app.get("/metrics")
     async def metrics():
-        return PlainTextResponse(worker.metrics.prometheus())
+        from ..utils import levers
+        return PlainTextResponse(worker.metrics.prometheus(worker.engine.stats, levers.switches()))
 
     return app
 

@@ -47,3 +47,4 @@ def test_chat_and_models_and_metrics(client):
     assert client.get("/v1/models").json()["data"][0]["id"] == "tiny"
     m = client.get("/metrics").text
     assert "b200ds_requests_completed_total" in m
+    assert "b200ds_engine_decode_tokens_total" in m and 'b200ds_switch{name="moe_fused"}' in m
