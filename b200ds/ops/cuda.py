@@ -118,15 +118,19 @@ def _gemm_raw(a, w: MXFP8Tensor, out: torch.Tensor, epi: int, splits: int = 1, p
             None, None, 0, None, None, pdl)
 
 
-def choose_splits(T: int, N: int, K: int) -> int:
+def choose_splits(T: int, N: int, K: int, max_ctas: int = 2 * 148) -> int:
     """Cluster split-K factor (1, 2, 4 or 8) so small-token GEMMs cover the
-    148 SMs; every split keeps at least two k-tiles."""
+    148 SMs: the largest factor whose CTAs all stay resident at once (the
+    split-K kernels fit two CTAs per SM); every split keeps at least two
+    k-tiles.  (o_proj at N = 7168: 4 splits, 224 CTAs; at 2 splits only 112
+    SMs streamed weights, 0.47 of copy bandwidth under ncu.)  max_ctas caps
+    the grid (the push epilogue's GEMM keeps its 1.5-wave cap)."""
     if T > 128:
         return 1
     tiles = N // 128
     ktiles = K // 128
     s = 1
-    while s < 8 and tiles * s * 2 <= 148 + 74 and ktiles // (s * 2) >= 2:
+    while s < 8 and tiles * s * 2 <= max_ctas and ktiles // (s * 2) >= 2:
         s *= 2
     return s
 

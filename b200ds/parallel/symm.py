@@ -90,7 +90,7 @@ class FusedAllReduce:
         a = x if isinstance(x, QAct) else quant(x)
         T, K = a.q.shape
         N = wq.data.shape[0]
-        splits = choose_splits(T, N, K)
+        splits = choose_splits(T, N, K, max_ctas=148 + 74)
         if splits < 2 or T > 128:
             from ..ops.cuda import gemm
             return self.allreduce_add_rmsnorm(gemm(a, wq), residual, ln_w, eps, quantize)
