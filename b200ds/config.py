@@ -300,6 +300,7 @@ class EngineConfig:
     max_model_len: int = 16384       # longest sequence (sizes graph block tables)
     max_num_seqs: int = 256          # concurrent running requests
     max_prefill_tokens: int = 16384  # chunked-prefill budget per step
+    mixed_steps: bool = False        # prefill steps also advance running requests by one decode token
     kv_cache_fraction: float = 0.85  # of free HBM after weights
     max_kv_pages: Optional[int] = None
     cuda_graphs: bool = True         # capture decode per batch bucket

@@ -67,7 +67,8 @@ class Engine:
                 raise ValueError("spec_mtp runs without the prefix cache")
             self.mtp.allocate_kv(num_pages)
         self.radix = RadixCache(self.pool) if ecfg.enable_prefix_cache else None
-        self.sched = Scheduler(self.pool, ecfg.max_num_seqs, ecfg.max_prefill_tokens, self.radix)
+        self.sched = Scheduler(self.pool, ecfg.max_num_seqs, ecfg.max_prefill_tokens, self.radix,
+                               mixed=ecfg.mixed_steps and not ecfg.dp_attention and not ecfg.spec_mtp)
         self.eos = eos_token_id
         self.tokenizer = tokenizer
         self._next_rid = 0
@@ -219,7 +220,9 @@ class Engine:
         done = []
         self.stats["steps"] += 1
         if st.kind == "prefill":
-            self.stats["prefill_tokens"] += sum(len(c) for c in st.chunks)
+            n_pre = len(st.chunks) - st.decode_rows
+            self.stats["prefill_tokens"] += sum(len(c) for c in st.chunks[:n_pre])
+            self.stats["decode_tokens"] += st.decode_rows
         else:
             self.stats["decode_tokens"] += sum(len(m) for m in multi)
         for r, smp, new in zip(st.reqs, st.sample, multi):

@@ -27,6 +27,7 @@ class Step:
     chunks: List[List[int]]        # new tokens per request
     starts: List[int]              # cached length before the step
     sample: List[bool]             # whether the step's last logits produce a token
+    decode_rows: int = 0           # mixed prefill step: its last rows are running requests' decode tokens
 
 
 def prefill_target(r: Request) -> int:
@@ -38,8 +39,11 @@ def prefill_target(r: Request) -> int:
 
 class Scheduler:
     def __init__(self, pool: PagePool, max_num_seqs: int, max_prefill_tokens: int,
-                 radix: Optional[RadixCache] = None):
+                 radix: Optional[RadixCache] = None, mixed: bool = False):
         self.pool = pool
+        # mixed = True: a prefill step also carries one decode token of every
+        # running request, so decoding does not stall behind long prompts
+        self.mixed = mixed
         self.radix = radix
         self.max_num_seqs = max_num_seqs
         self.max_prefill_tokens = max_prefill_tokens
@@ -98,6 +102,9 @@ class Scheduler:
     # ------------------------------------------------------------------
     def next_step(self) -> Optional[Step]:
         budget = self.max_prefill_tokens
+        if self.mixed and self.running:
+            # the running requests' decode tokens ride along: reserve them
+            budget = max(1, budget - len(self.running))
         if self.prefilling or (self.waiting and len(self.running) + len(self.prefilling) < self.max_num_seqs):
             reqs, chunks, starts, sample = [], [], [], []
             cands = list(self.prefilling)
@@ -127,7 +134,18 @@ class Scheduler:
                 sample.append(r.cached + n == target and not r.output)
                 budget -= n
             if reqs:
-                return Step("prefill", reqs, chunks, starts, sample)
+                nd = 0
+                if self.mixed:
+                    for r in self.running:
+                        if not self._ensure_pages(r, r.cached + 1):
+                            continue
+                        reqs.append(r)
+                        chunks.append([r.all_tokens[r.cached]])
+                        starts.append(r.cached)
+                        sample.append(True)
+                        budget -= 1
+                        nd += 1
+                return Step("prefill", reqs, chunks, starts, sample, decode_rows=nd)
         if not self.running:
             if self.has_work:
                 raise OutOfPages("no request fits in the KV pool")
@@ -148,9 +166,10 @@ class Scheduler:
 
     def commit(self, step: Step) -> None:
         """Advance cached lengths after the forward ran."""
-        for r, ch in zip(step.reqs, step.chunks):
+        n_pre = len(step.reqs) - step.decode_rows
+        for i, (r, ch) in enumerate(zip(step.reqs, step.chunks)):
             r.cached += len(ch)
-            if step.kind == "prefill":
+            if step.kind == "prefill" and i < n_pre:
                 if r.cached >= prefill_target(r):
                     self.running.append(r)
                 else:

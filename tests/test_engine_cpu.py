@@ -123,3 +123,27 @@ def test_stop_tokens_and_seeded_sampling():
     a = eng.generate([prompt], sp)[0].token_ids
     b = eng.generate([prompt], sp)[0].token_ids
     assert a == b
+
+
+def test_mixed_steps_same_tokens_and_no_decode_stall():
+    """Mixed steps: while a long prompt prefills in chunks, running requests
+    keep decoding (one token per step) and every request gets the tokens of
+    the prefill-first schedule."""
+    def run(mixed):
+        eng, cfg = _engine(False, mixed_steps=mixed, max_prefill_tokens=6)
+        from b200ds.engine.request import SamplingParams
+        a = eng.add_request(list(range(3, 12)), SamplingParams(max_tokens=12))
+        for _ in range(3):
+            eng.step()
+        b = eng.add_request(list(range(100, 140)), SamplingParams(max_tokens=4))
+        grew = []
+        while not (a.finished and b.finished):
+            n = len(a.output)
+            eng.step()
+            if b.t_first is None and not a.finished:
+                grew.append(len(a.output) > n)
+        return a.output, b.output, grew
+    a0, b0, g0 = run(False)
+    a1, b1, g1 = run(True)
+    assert a1 == a0 and b1 == b0
+    assert all(g1) and not all(g0)          # prefill-first stalls a's decoding; mixed does not
