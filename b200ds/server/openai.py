@@ -365,6 +365,8 @@ def main(argv=None):
     ap.add_argument("--spec-mtp", action="store_true", help="speculative decoding with the model's MTP module")
     ap.add_argument("--spec-k", type=int, default=4, help="draft tokens verified per step")
     ap.add_argument("--trace", action="store_true", help="device timestamps per layer phase")
+    ap.add_argument("--mixed-steps", action="store_true", help="decode tokens ride along with prefill chunks")
+    ap.add_argument("--extend-graphs", action="store_true", help="replay prefill chunks from CUDA graphs")
     args = ap.parse_args(argv)
     import uvicorn
     from .. import load_engine
@@ -376,7 +378,8 @@ def main(argv=None):
                         dp_attention=args.dp_attention, max_num_seqs=args.max_num_seqs,
                         cuda_graphs=not args.no_cuda_graphs, max_model_len=args.max_model_len,
                         enable_prefix_cache=not (args.no_prefix_cache or args.spec_mtp),
-                        spec_ngram=args.spec_ngram, spec_mtp=args.spec_mtp, spec_k=args.spec_k, trace=args.trace)
+                        spec_ngram=args.spec_ngram, spec_mtp=args.spec_mtp, spec_k=args.spec_k, trace=args.trace,
+                        mixed_steps=args.mixed_steps, extend_graphs=args.extend_graphs)
     eng = load_engine(args.model, weights=args.weights, ecfg=ecfg)
     tok = load_tokenizer(args.model)
     eng.tokenizer = tok
