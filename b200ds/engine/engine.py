@@ -113,6 +113,16 @@ class Engine:
         self.sched.add(r)
         return r
 
+    def abort(self, r: Request) -> None:
+        """Stop a request now (client gone): it leaves the schedule, its pages
+        are freed, finish_reason becomes "abort".  Call between steps; SPMD
+        ranks must abort the same requests in the same order."""
+        if r.finished:
+            return
+        self.sched.abort(r)
+        r.finished, r.finish_reason = True, "abort"
+        r.t_done = time.perf_counter()
+
     def _forward(self, step: Step) -> List[int]:
         seqs = [{"tokens": ch, "start": st, "pages": r.pages}
                 for r, ch, st in zip(step.reqs, step.chunks, step.starts)]

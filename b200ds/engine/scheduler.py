@@ -175,6 +175,17 @@ class Scheduler:
                 else:
                     self.prefilling.append(r)
 
+    def abort(self, r: Request) -> None:
+        """Drop a request wherever it is (waiting, mid-prefill, running) and
+        free its pages (fully computed pages still enter the prefix cache)."""
+        for lst in (self.running, self.prefilling):
+            if r in lst:
+                lst.remove(r)
+        if r in self.waiting:
+            self.waiting.remove(r)
+        if r.pages:
+            self.release(r)
+
     def finish(self, r: Request) -> None:
         if r in self.running:
             self.running.remove(r)

@@ -39,6 +39,7 @@ class EngineWorker:
         self.tok = tokenizer
         self.ps = ps
         self.inbox: "queue.Queue" = queue.Queue()
+        self.cancels: "queue.Queue" = queue.Queue()     # subscription queues whose client went away
         self.subs: Dict[int, tuple] = {}     # rid -> (loop, asyncio.Queue, emitted count)
         self._stop = threading.Event()
         self.t = threading.Thread(target=self._run, daemon=True)
@@ -55,6 +56,29 @@ class EngineWorker:
     def submit(self, prompt_ids: List[int], params: SamplingParams, loop, q) -> None:
         self.inbox.put((prompt_ids, params, loop, q))
 
+    def cancel(self, q) -> None:
+        """The client of subscription q is gone: abort its request."""
+        self.cancels.put(q)
+
+    def _cancelled(self) -> List[int]:
+        """Keys of self.subs whose client is gone (drained from the cancel
+        queue; subscriptions not admitted yet are aborted when they are)."""
+        gone = []
+        while True:
+            try:
+                gone.append(self.cancels.get_nowait())
+            except queue.Empty:
+                break
+        if gone:
+            self._pending_cancel = getattr(self, "_pending_cancel", []) + gone
+        pend = getattr(self, "_pending_cancel", [])
+        keys, keep = [], []
+        for q in pend:
+            k = next((key for key, sub in self.subs.items() if sub[1] is q), None)
+            (keys if k is not None else keep).append(k if k is not None else q)
+        self._pending_cancel = keep
+        return keys
+
     def _admit(self) -> List[tuple]:
         new = []
         while True:
@@ -68,12 +92,18 @@ class EngineWorker:
         eng = self.engine
         while not self._stop.is_set():
             new = self._admit()
-            if self.ps is not None and self.ps.world_size > 1:
-                _broadcast_requests(self.ps, [(p, sp.__dict__) for p, sp, _, _ in new])
             for prompt, params, loop, q in new:
                 r = eng.add_request(prompt, params)
                 self.subs[r.rid] = (loop, q, 0, r)
                 self.metrics.requests += 1
+            aborts = self._cancelled()
+            if self.ps is not None and self.ps.world_size > 1:
+                # followers mirror admissions in order, so rids agree across ranks
+                _broadcast_requests(self.ps, {"new": [(p, sp.__dict__) for p, sp, _, _ in new], "abort": aborts})
+            for rid in aborts:
+                loop, q, _, r = self.subs.pop(rid)
+                eng.abort(r)
+                loop.call_soon_threadsafe(q.put_nowait, ("done", "abort"))
             if not eng.sched.has_work:
                 time.sleep(0.002)
                 continue
@@ -124,8 +154,13 @@ class DPEngineWorker(EngineWorker):
                 self.subs[gid] = (loop, q, 0, None)
                 self.metrics.requests += 1
                 batch.append((prompt, params.__dict__, gid % world, gid))
-            _broadcast_requests(ps, batch)
+            aborts = self._cancelled()
+            _broadcast_requests(ps, {"new": batch, "abort": aborts})
             _dp_admit(eng, ps, batch, self.own)
+            _dp_abort(eng, aborts, self.own)
+            for gid in aborts:
+                loop, q, _, _ = self.subs.pop(gid)
+                loop.call_soon_threadsafe(q.put_nowait, ("done", "abort"))
             t0 = time.perf_counter()
             eng.step()
             if eng.sched.has_work:
@@ -143,6 +178,13 @@ class DPEngineWorker(EngineWorker):
             if not new and not self.subs:
                 time.sleep(0.002)
         _broadcast_requests(ps, None)           # followers stop
+
+
+def _dp_abort(eng, gids, own) -> None:
+    for gid in gids:
+        st = own.pop(gid, None)
+        if st is not None:
+            eng.abort(st[0])
 
 
 def _dp_admit(eng, ps, batch, own) -> None:
@@ -176,10 +218,11 @@ def dp_follower_loop(engine, ps) -> None:
     lockstep with rank 0 and send it this rank's new tokens every step."""
     own: Dict[int, list] = {}
     while True:
-        batch = _broadcast_requests(ps, [])
-        if batch is None:
+        msg = _broadcast_requests(ps, None)
+        if msg is None:
             return
-        _dp_admit(engine, ps, batch, own)
+        _dp_admit(engine, ps, msg["new"], own)
+        _dp_abort(engine, msg["abort"], own)
         engine.step()
         _dp_gather(ps, _dp_updates(own))
 
@@ -189,12 +232,20 @@ def follower_loop(engine, ps) -> None:
     attention engines serve their own share (dp_follower_loop)."""
     if getattr(engine, "dp", False):
         return dp_follower_loop(engine, ps)
+    reqs_by_rid = {}
     while True:
-        reqs = _broadcast_requests(ps, None)
-        if reqs is None:
+        msg = _broadcast_requests(ps, None)
+        if msg is None:
             return
-        for prompt, spd in reqs:
-            engine.add_request(prompt, SamplingParams(**spd))
+        for prompt, spd in msg["new"]:
+            r = engine.add_request(prompt, SamplingParams(**spd))
+            reqs_by_rid[r.rid] = r
+        for rid in msg["abort"]:
+            r = reqs_by_rid.pop(rid, None)
+            if r is not None:
+                engine.abort(r)
+        if len(reqs_by_rid) > 1024:
+            reqs_by_rid = {k: r for k, r in reqs_by_rid.items() if not r.finished}
         if engine.sched.has_work:
             engine.step()
 
@@ -296,6 +347,16 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
         obj = "chat.completion" if chat else "text_completion"
         if body.get("stream"):
             async def gen():
+                done = False
+                try:
+                    async for chunk in _chunks():
+                        yield chunk
+                    done = True
+                finally:
+                    if not done:              # client disconnected: free the request
+                        worker.cancel(q)
+
+            async def _chunks():
                 while True:
                     kind, val = await q.get()
                     if kind == "tokens":
@@ -312,13 +373,17 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
             return StreamingResponse(gen(), media_type="text/event-stream")
         out: List[int] = []
         reason = "length"
-        while True:
-            kind, val = await q.get()
-            if kind == "tokens":
-                out.extend(val)
-            else:
-                reason = val
-                break
+        try:
+            while True:
+                kind, val = await q.get()
+                if kind == "tokens":
+                    out.extend(val)
+                else:
+                    reason = val
+                    break
+        except BaseException:              # cancelled (client gone)
+            worker.cancel(q)
+            raise
         text = tok.decode(out)
         choice = ({"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": reason} if chat
                   else {"index": 0, "text": text, "token_ids": out, "finish_reason": reason})

@@ -147,3 +147,59 @@ def test_mixed_steps_same_tokens_and_no_decode_stall():
     a1, b1, g1 = run(True)
     assert a1 == a0 and b1 == b0
     assert all(g1) and not all(g0)          # prefill-first stalls a's decoding; mixed does not
+
+
+def test_abort_waiting_prefilling_running():
+    """Aborting frees the request's pages wherever it is; the others finish
+    with their usual tokens."""
+    from b200ds.engine.request import SamplingParams
+    eng, cfg = _engine(False, max_prefill_tokens=8)
+    free0 = eng.pool.num_free
+    ref_eng, _ = _engine(False, max_prefill_tokens=8)
+    keep_ref = ref_eng.generate([list(range(5, 25))], SamplingParams(max_tokens=6))[0].token_ids
+    keep = eng.add_request(list(range(5, 25)), SamplingParams(max_tokens=6))
+    mid = eng.add_request(list(range(30, 60)), SamplingParams(max_tokens=6))
+    late = eng.add_request(list(range(70, 80)), SamplingParams(max_tokens=6))
+    eng.step()                                   # keep is mid-prefill, mid / late wait
+    eng.abort(late)                              # waiting
+    eng.step()
+    eng.abort(mid)                               # prefilling
+    while not keep.finished:
+        eng.step()
+    assert keep.output == keep_ref
+    assert late.finish_reason == "abort" and mid.finish_reason == "abort"
+    run = eng.add_request(list(range(90, 100)), SamplingParams(max_tokens=50))
+    for _ in range(4):
+        eng.step()
+    eng.abort(run)                               # running
+    assert not eng.sched.has_work and eng.pool.num_free == free0
+
+
+def test_server_cancel_aborts_request():
+    """A subscription whose client went away is aborted by the worker."""
+    import asyncio
+    import time as _t
+    from b200ds.engine.request import SamplingParams
+    from b200ds.server.openai import EngineWorker
+    eng, cfg = _engine(False)
+
+    class Loop:
+        def __init__(self):
+            self.items = []
+
+        def call_soon_threadsafe(self, fn, item):
+            fn(item)
+
+        def put_nowait(self, item):
+            self.items.append(item)
+    w = EngineWorker(eng, None).start()
+    lp = Loop()
+    w.submit(list(range(40)), SamplingParams(max_tokens=10000), lp, lp)
+    t0 = _t.time()
+    while not any(k == "tokens" for k, _ in lp.items) and _t.time() - t0 < 60:
+        _t.sleep(0.01)
+    w.cancel(lp)
+    while not any(k == "done" for k, _ in lp.items) and _t.time() - t0 < 60:
+        _t.sleep(0.01)
+    w.stop()
+    assert ("done", "abort") in lp.items and not eng.sched.has_work
