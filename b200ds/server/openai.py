@@ -103,7 +103,7 @@ class EngineWorker:
             for rid in aborts:
                 loop, q, _, r = self.subs.pop(rid)
                 eng.abort(r)
-                loop.call_soon_threadsafe(q.put_nowait, ("done", "abort"))
+                _post(loop, q, ("done", "abort"))
             if not eng.sched.has_work:
                 time.sleep(0.002)
                 continue
@@ -111,16 +111,29 @@ class EngineWorker:
             done = eng.step()
             self.metrics.step_time.append(time.perf_counter() - t0)
             for rid, (loop, q, sent, r) in list(self.subs.items()):
+                alive = True
                 if len(r.output) > sent:
                     new_toks = r.output[sent:]
                     self.subs[rid] = (loop, q, len(r.output), r)
-                    loop.call_soon_threadsafe(q.put_nowait, ("tokens", new_toks))
+                    alive = _post(loop, q, ("tokens", new_toks))
                 if r.finished:
-                    loop.call_soon_threadsafe(q.put_nowait, ("done", r.finish_reason))
+                    _post(loop, q, ("done", r.finish_reason))
                     self.metrics.finish(r)
                     del self.subs[rid]
+                elif not alive:               # the handler's event loop is gone
+                    self.cancel(q)
         if self.ps is not None and self.ps.world_size > 1:
             _broadcast_requests(self.ps, None)      # followers stop
+
+
+def _post(loop, q, item) -> bool:
+    """Hand an event to a request handler's event loop; False when that loop
+    has closed (the client is gone)."""
+    try:
+        loop.call_soon_threadsafe(q.put_nowait, item)
+        return True
+    except RuntimeError:
+        return False
 
 
 def _broadcast_requests(ps, reqs):
@@ -160,18 +173,21 @@ class DPEngineWorker(EngineWorker):
             _dp_abort(eng, aborts, self.own)
             for gid in aborts:
                 loop, q, _, _ = self.subs.pop(gid)
-                loop.call_soon_threadsafe(q.put_nowait, ("done", "abort"))
+                _post(loop, q, ("done", "abort"))
             t0 = time.perf_counter()
             eng.step()
             if eng.sched.has_work:
                 self.metrics.step_time.append(time.perf_counter() - t0)
             for upd in _dp_gather(ps, _dp_updates(self.own)):
                 for gid, toks, fin, reason, r in upd:
+                    if gid not in self.subs:     # aborted meanwhile
+                        continue
                     loop, q, sent, _ = self.subs[gid]
-                    if toks:
-                        loop.call_soon_threadsafe(q.put_nowait, ("tokens", toks))
+                    alive = _post(loop, q, ("tokens", toks)) if toks else True
+                    if not alive and not fin:
+                        self.cancel(q)
                     if fin:
-                        loop.call_soon_threadsafe(q.put_nowait, ("done", reason))
+                        _post(loop, q, ("done", reason))
                         if r is not None:
                             self.metrics.finish(r)
                         del self.subs[gid]
@@ -295,6 +311,23 @@ class _Metrics:
         return "\n".join(lines) + "\n"
 
 
+def _stop_scan(text: str, stops: List[str]):
+    """(index of the first stop string in text or None, length of the longest
+    text suffix that is a prefix of a stop string: held back from streaming)."""
+    cut = None
+    for st in stops:
+        i = text.find(st)
+        if i >= 0 and (cut is None or i < cut):
+            cut = i
+    hold = 0
+    for st in stops:
+        for n in range(min(len(st) - 1, len(text)), 0, -1):
+            if text.endswith(st[:n]):
+                hold = max(hold, n)
+                break
+    return cut, hold
+
+
 def _params(body: dict, default_max: int = 16) -> SamplingParams:
     stop_ids = body.get("stop_token_ids") or []
     return SamplingParams(
@@ -345,6 +378,8 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
         created = int(time.time())
         q = await _run(ids, params)
         obj = "chat.completion" if chat else "text_completion"
+        stops = body.get("stop") or []
+        stops = [stops] if isinstance(stops, str) else [x for x in stops if isinstance(x, str) and x]
         if body.get("stream"):
             async def gen():
                 done = False
@@ -357,13 +392,28 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
                         worker.cancel(q)
 
             async def _chunks():
+                ids_all: List[int] = []
+                sent = 0                      # characters of the decoded text already streamed
                 while True:
                     kind, val = await q.get()
                     if kind == "tokens":
-                        text = tok.decode(val)
-                        choice = ({"index": 0, "delta": {"content": text}, "finish_reason": None} if chat
-                                  else {"index": 0, "text": text, "token_ids": val, "finish_reason": None})
-                        yield f"data: {json.dumps({'id': rid, 'object': obj + '.chunk', 'created': created, 'model': model_name, 'choices': [choice]})}\n\n"
+                        ids_all.extend(val)
+                        full = tok.decode(ids_all)
+                        cut, hold = _stop_scan(full, stops)
+                        end = cut if cut is not None else len(full) - hold
+                        text = full[sent:end] if end > sent else ""
+                        sent = max(sent, end)
+                        if text or cut is None:
+                            choice = ({"index": 0, "delta": {"content": text}, "finish_reason": None} if chat
+                                      else {"index": 0, "text": text, "token_ids": val, "finish_reason": None})
+                            yield f"data: {json.dumps({'id': rid, 'object': obj + '.chunk', 'created': created, 'model': model_name, 'choices': [choice]})}\n\n"
+                        if cut is not None:     # a stop string: finish now and free the request
+                            worker.cancel(q)
+                            choice = ({"index": 0, "delta": {}, "finish_reason": "stop"} if chat
+                                      else {"index": 0, "text": "", "finish_reason": "stop"})
+                            yield f"data: {json.dumps({'id': rid, 'object': obj + '.chunk', 'created': created, 'model': model_name, 'choices': [choice]})}\n\n"
+                            yield "data: [DONE]\n\n"
+                            return
                     else:
                         choice = ({"index": 0, "delta": {}, "finish_reason": val} if chat
                                   else {"index": 0, "text": "", "finish_reason": val})
@@ -373,18 +423,25 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
             return StreamingResponse(gen(), media_type="text/event-stream")
         out: List[int] = []
         reason = "length"
+        text = None
         try:
             while True:
                 kind, val = await q.get()
                 if kind == "tokens":
                     out.extend(val)
+                    if stops:
+                        cut, _ = _stop_scan(tok.decode(out), stops)
+                        if cut is not None:
+                            text, reason = tok.decode(out)[:cut], "stop"
+                            worker.cancel(q)
+                            break
                 else:
                     reason = val
                     break
         except BaseException:              # cancelled (client gone)
             worker.cancel(q)
             raise
-        text = tok.decode(out)
+        text = tok.decode(out) if text is None else text
         choice = ({"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": reason} if chat
                   else {"index": 0, "text": text, "token_ids": out, "finish_reason": reason})
         return JSONResponse({"id": rid, "object": obj, "created": created, "model": model_name, "choices": [choice],

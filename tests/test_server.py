@@ -48,3 +48,24 @@ def test_chat_and_models_and_metrics(client):
     m = client.get("/metrics").text
     assert "b200ds_requests_completed_total" in m
     assert "b200ds_engine_decode_tokens_total" in m and 'b200ds_switch{name="moe_fused"}' in m
+
+
+def test_stop_strings(client):
+    """A stop string ends the completion (text cut before it, finish_reason
+    stop) in both the plain and the streamed response."""
+    from b200ds.engine.tokenizer import ByteTokenizer
+    tok = ByteTokenizer()
+    base = client.post("/v1/completions", json={"prompt": [9, 10, 11], "max_tokens": 8, "temperature": 0}).json()
+    ids = base["choices"][0]["token_ids"]
+    text = tok.decode(ids)
+    stop = tok.decode(ids[3:5])
+    k = text.find(stop)
+    assert k >= 0
+    r = client.post("/v1/completions", json={"prompt": [9, 10, 11], "max_tokens": 8, "temperature": 0,
+                                             "stop": stop}).json()
+    assert r["choices"][0]["finish_reason"] == "stop" and r["choices"][0]["text"] == text[:k]
+    with client.stream("POST", "/v1/completions", json={"prompt": [9, 10, 11], "max_tokens": 8, "temperature": 0,
+                                                        "stop": [stop], "stream": True}) as s:
+        events = [json.loads(l[6:]) for l in s.iter_lines() if l.startswith("data: ") and l != "data: [DONE]"]
+    assert "".join(e["choices"][0]["text"] for e in events) == text[:k]
+    assert events[-1]["choices"][0]["finish_reason"] == "stop"
