@@ -357,11 +357,13 @@ _ERR_WORDS = []     # device error words of kernels with in-kernel waits
 
 
 def check_device_errors() -> None:
-    """Raise if a bounded in-kernel wait (dependency between CTAs) ran out."""
-    for e in _ERR_WORDS:
-        v = int(e.item())
-        if v:
-            raise RuntimeError(f"fused expert GEMM: in-kernel dependency wait timed out (code {v})")
+    """Raise if a bounded in-kernel wait (dependency between CTAs) ran out.
+    One device read for all error words (one per expert set)."""
+    if not _ERR_WORDS:
+        return
+    v = int(torch.cat(_ERR_WORDS).max().item()) if len(_ERR_WORDS) > 1 else int(_ERR_WORDS[0].item())
+    if v:
+        raise RuntimeError(f"fused expert GEMM: in-kernel dependency wait timed out (code {v})")
 
 
 def _expert_gemms(ex, xq, xsf, xg, hq, hsf, y, Hd, bn1, bn2, seg_start, seg_count, tt1, tt2, row_weight, fp4,
