@@ -311,6 +311,8 @@ def router(x: torch.Tensor, gate: torch.Tensor, bias: torch.Tensor, cfg):
         # tcgen05 split-K GEMM (fp32 accumulate across splits)
         logits = torch.zeros(T, E, dtype=torch.float32, device=x.device)
         splits = max(1, min(32, (Kd // 64) // 4, 148 // max(1, (E // 128) * -(-T // 128))))
+        if levers.on("deterministic"):
+            splits = 1             # fp32 atomics from several splits sum in any order
         _C.bf16_absorb(g16.view(1, E, Kd), xb.view(T, 1, Kd), 3, logits.view(T, 1, E), None, None, None, None,
                        None, None, None, splits=splits)
     else:
@@ -730,6 +732,8 @@ def hc_pre(X, sumsq, hw, norm_w, eps, cfg, next_linear, head, keep_hf):
         parts = hw.fn_parts = hc_fn_parts(hw.fn)
     raw = torch.zeros(T, 128, dtype=torch.float32, device=X.device)
     splits = max(1, min(32, (K // 64) // 4, 148 // max(1, -(-T // 128))))
+    if levers.on("deterministic"):
+        splits = 1
     _C.bf16_absorb(parts.view(1, 128, K), X.view(T, 1, K), 3, raw.view(T, 1, 128), None, None, None, None, None,
                    None, None, splits=splits)
     quantized = next_linear is not None and getattr(next_linear, "quantized", False)

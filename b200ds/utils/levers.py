@@ -120,3 +120,6 @@ register("moe_pull", "B200_MOE_PULL", True,
          "fused experts read FC1 rows in place (activations / EP dispatch buffer) instead of a sorted copy")
 register("fused_comm", "B200_FUSED_COMM", True,
          "device-initiated NVLink collectives fused into the producing / consuming kernels")
+register("deterministic", "B200_DETERMINISTIC", False,
+         "bitwise-reproducible steps: split-K GEMMs that sum with fp32 atomics (router logits, mHC stats) run "
+         "unsplit")
