@@ -131,11 +131,13 @@ class DeepseekModel:
         # boundary.  ps_local is the single-rank view for local reductions.
         self.dp = bool(ecfg.dp_attention) and ps.ep_size > 1
         self.ps_local = ParallelState(device=self.device) if self.dp else ps
-        if (self.device.type == "cuda" and ps.tp_size > 1 and ecfg.comm_impl == "fused"
+        from ..utils import levers
+        fused_comm = ecfg.comm_impl == "fused" and levers.on("fused_comm")
+        if (self.device.type == "cuda" and ps.tp_size > 1 and fused_comm
                 and getattr(ps, "fused_ar", None) is None):
             from ..parallel.symm import FusedAllReduce
             ps.fused_ar = FusedAllReduce(ps, cfg.hidden_size, max_tokens=max(ecfg.max_num_seqs, 256))
-        if (self.device.type == "cuda" and self.dp and ecfg.comm_impl == "fused" and cfg.n_routed_experts
+        if (self.device.type == "cuda" and self.dp and fused_comm and cfg.n_routed_experts
                 and getattr(ps, "fused_ep", None) is None):
             from ..parallel.symm import EPDispatch, FusedAllReduce
             cap = max(ecfg.max_num_seqs, 256)
