@@ -370,16 +370,58 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
             raise HTTPException(400, "prompt must be a string or a list of token ids")
         return tok.encode(p)
 
+    async def _collect(q, stops):
+        """Tokens of one subscription until it finishes (or a stop string
+        appears): (token ids, text, finish reason)."""
+        out: List[int] = []
+        reason = "length"
+        text = None
+        try:
+            while True:
+                kind, val = await q.get()
+                if kind == "tokens":
+                    out.extend(val)
+                    if stops:
+                        cut, _ = _stop_scan(tok.decode(out), stops)
+                        if cut is not None:
+                            text, reason = tok.decode(out)[:cut], "stop"
+                            worker.cancel(q)
+                            break
+                else:
+                    reason = val
+                    break
+        except BaseException:              # cancelled (client gone)
+            worker.cancel(q)
+            raise
+        return out, (tok.decode(out) if text is None else text), reason
+
     async def _handle(request: Request, chat: bool):
         body = await request.json()
         ids = _prompt_ids(body, chat)
         params = _params(body)
         rid = f"{'chatcmpl' if chat else 'cmpl'}-{uuid.uuid4().hex[:16]}"
         created = int(time.time())
-        q = await _run(ids, params)
+        n = int(body.get("n") or 1)
+        if n < 1 or (n > 1 and body.get("stream")):
+            raise HTTPException(400, "n must be >= 1 (and 1 when streaming)")
         obj = "chat.completion" if chat else "text_completion"
         stops = body.get("stop") or []
         stops = [stops] if isinstance(stops, str) else [x for x in stops if isinstance(x, str) and x]
+        if n > 1:
+            # n independent samples of the prompt (seed + i when a seed is given)
+            import dataclasses
+            qs = [await _run(ids, dataclasses.replace(params, seed=None if params.seed is None else params.seed + i))
+                  for i in range(n)]
+            results = [await _collect(q, stops) for q in qs]
+            choices = []
+            for i, (out, text, reason) in enumerate(results):
+                choices.append({"index": i, "message": {"role": "assistant", "content": text}, "finish_reason": reason}
+                               if chat else {"index": i, "text": text, "token_ids": out, "finish_reason": reason})
+            gen_tok = sum(len(o) for o, _, _ in results)
+            return JSONResponse({"id": rid, "object": obj, "created": created, "model": model_name,
+                                 "choices": choices, "usage": {"prompt_tokens": len(ids), "completion_tokens": gen_tok,
+                                                               "total_tokens": len(ids) + gen_tok}})
+        q = await _run(ids, params)
         if body.get("stream"):
             async def gen():
                 done = False
@@ -421,27 +463,7 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
                         yield "data: [DONE]\n\n"
                         return
             return StreamingResponse(gen(), media_type="text/event-stream")
-        out: List[int] = []
-        reason = "length"
-        text = None
-        try:
-            while True:
-                kind, val = await q.get()
-                if kind == "tokens":
-                    out.extend(val)
-                    if stops:
-                        cut, _ = _stop_scan(tok.decode(out), stops)
-                        if cut is not None:
-                            text, reason = tok.decode(out)[:cut], "stop"
-                            worker.cancel(q)
-                            break
-                else:
-                    reason = val
-                    break
-        except BaseException:              # cancelled (client gone)
-            worker.cancel(q)
-            raise
-        text = tok.decode(out) if text is None else text
+        out, text, reason = await _collect(q, stops)
         choice = ({"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": reason} if chat
                   else {"index": 0, "text": text, "token_ids": out, "finish_reason": reason})
         return JSONResponse({"id": rid, "object": obj, "created": created, "model": model_name, "choices": [choice],

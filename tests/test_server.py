@@ -69,3 +69,13 @@ def test_stop_strings(client):
         events = [json.loads(l[6:]) for l in s.iter_lines() if l.startswith("data: ") and l != "data: [DONE]"]
     assert "".join(e["choices"][0]["text"] for e in events) == text[:k]
     assert events[-1]["choices"][0]["finish_reason"] == "stop"
+
+
+def test_n_choices(client):
+    r = client.post("/v1/completions", json={"prompt": [3, 4, 5], "max_tokens": 4, "temperature": 0.9,
+                                             "seed": 11, "n": 3}).json()
+    assert [c["index"] for c in r["choices"]] == [0, 1, 2]
+    assert all(len(c["token_ids"]) == 4 for c in r["choices"]) and r["usage"]["completion_tokens"] == 12
+    again = client.post("/v1/completions", json={"prompt": [3, 4, 5], "max_tokens": 4, "temperature": 0.9,
+                                                 "seed": 11, "n": 3}).json()
+    assert [c["token_ids"] for c in again["choices"]] == [c["token_ids"] for c in r["choices"]]
