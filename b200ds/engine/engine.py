@@ -276,8 +276,9 @@ class Engine:
         (logits at every position).  Returns the accepted tokens per request
         (accepted draft prefix + the model's next token), or None when no
         request has a draft (plain decode then)."""
-        if self.dp or not st.reqs or any(r.params.temperature > 0 for r in st.reqs):
+        if self.dp or not st.reqs:
             return None
+        sampling = any(r.params.temperature > 0 for r in st.reqs)
         drafts = []
         for r in st.reqs:
             room = r.params.max_tokens - len(r.output) - 1
@@ -290,7 +291,7 @@ class Engine:
         seqs = [{"tokens": ch + d, "start": s, "pages": r.pages}
                 for r, ch, s, d in zip(st.reqs, st.chunks, st.starts, drafts)]
         k = self.ecfg.spec_k
-        if self.graphs is not None and self.verify_graphs_ok:
+        if self.graphs is not None and self.verify_graphs_ok and not sampling:
             # fixed (1 + spec_k) rows per request: one captured graph per bucket
             if self.verify_graphs is None:
                 from .cuda_graph import VerifyGraphRunner
@@ -309,12 +310,54 @@ class Engine:
         fb = build_batch(seqs, self.ecfg.page_size, device="cpu")
         fb.last_idx = torch.arange(fb.num_tokens, dtype=torch.int64)     # logits at every position
         fb = self._to_device(fb)
-        pred = self.model.forward(fb).argmax(-1).tolist()
+        logits = self.model.forward(fb)
+        pred = logits.argmax(-1).tolist()
         starts, off = [], 0
         for d in drafts:
             starts.append(off)
             off += 1 + len(d)
+        if sampling:
+            return self._accept_sampled(st, drafts, logits, starts)
         return self._accept(st, drafts, pred, starts)
+
+    def _accept_sampled(self, st: Step, drafts, logits: torch.Tensor, starts: List[int]) -> List[List[int]]:
+        """Speculative sampling with deterministic (n-gram) drafts: draft token
+        d at a row is kept with probability p(d) under the request's sampling
+        distribution (temperature / top-k / top-p as the sampler applies
+        them); on rejection the row's token is drawn from p with d removed;
+        after a fully accepted draft the last row is sampled as usual.  The
+        accepted tokens follow the same distribution as plain sampling."""
+        from ..ops.ref import sampling_probs
+        out = []
+        lg = logits.float().cpu()
+        for r, d, off in zip(st.reqs, drafts, starts):
+            p = r.params
+            if p.temperature <= 0:
+                row = lg[off: off + 1 + len(d)].argmax(-1).tolist()
+                a = 0
+                while a < len(d) and row[a] == d[a]:
+                    a += 1
+                toks = d[:a] + [row[a]]
+            else:
+                toks = []
+                for j in range(len(d) + 1):
+                    probs = sampling_probs(lg[off + j], p.temperature, p.top_p, p.top_k)
+                    probs = probs / probs.sum()
+                    if j < len(d):
+                        if r.uniform() < float(probs[d[j]]):
+                            toks.append(d[j])
+                            continue
+                        probs = probs.clone()
+                        probs[d[j]] = 0.0
+                    c = probs.cumsum(0)
+                    u = r.uniform() * float(c[-1])
+                    toks.append(int(torch.searchsorted(c, torch.tensor([u])).clamp(max=probs.numel() - 1)))
+                    break
+                a = len(toks) - 1
+            out.append(toks)
+            self.stats["spec_proposed"] = self.stats.get("spec_proposed", 0) + len(d)
+            self.stats["spec_accepted"] = self.stats.get("spec_accepted", 0) + a
+        return out
 
     def _accept(self, st: Step, drafts, pred: List[int], starts: List[int]) -> List[List[int]]:
         """Greedy acceptance: the longest draft prefix the model reproduces,

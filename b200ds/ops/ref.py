@@ -149,6 +149,22 @@ def indexer_scores(q: torch.Tensor, w: torch.Tensor, k_cache: torch.Tensor, k_sc
 
 # -- sampling ----------------------------------------------------------------------------
 
+def sampling_probs(logits: torch.Tensor, temperature: float, top_p: float, top_k: int) -> torch.Tensor:
+    """The distribution `sample` draws from for one row: softmax(logits / T)
+    restricted to the top-k, then to the smallest prefix (by probability) whose
+    mass reaches top_p; unnormalised kept probabilities, zeros elsewhere."""
+    p = (logits.float() / temperature).softmax(-1)
+    sp, si = p.sort(descending=True)
+    keep = torch.ones_like(sp, dtype=torch.bool)
+    if top_k > 0:
+        keep[top_k:] = False
+    c = sp.cumsum(0)
+    keep &= (c - sp) < top_p
+    out = torch.zeros_like(p)
+    out[si[keep]] = sp[keep]
+    return out
+
+
 def sample(logits: torch.Tensor, temperature: torch.Tensor, top_p: torch.Tensor,
            top_k: torch.Tensor, uniform: torch.Tensor) -> torch.Tensor:
     """Per-row sampling with temperature (<=0 -> greedy), top-k (<=0 -> off)

@@ -139,3 +139,37 @@ def test_extend_batch_layout_matches_ragged():
     want = m.forward(build_batch(seqs, 8))
     got = m.forward(build_extend_batch(seqs, 32, 4, 8, 4))
     assert got.shape[0] == 4 and torch.allclose(got[:2], want, atol=1e-5)
+
+
+def test_speculative_sampling_preserves_distribution():
+    """Speculative sampling with a deterministic draft: the first verified
+    token follows the sampler's distribution p exactly (accept d with p(d),
+    else draw from p without d), and the token after an accepted draft
+    follows the next row's distribution."""
+    import types
+    import torch
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import Request, SamplingParams
+    from b200ds.ops.ref import sampling_probs
+    g = torch.Generator().manual_seed(0)
+    V = 8
+    logits = torch.randn(3, V, generator=g) * 2
+    params = SamplingParams(max_tokens=10, temperature=0.8, top_k=5, top_p=0.9, seed=1)
+    r = Request(0, [1, 2, 3], params)
+    eng = types.SimpleNamespace(stats={})
+    draft = [int(sampling_probs(logits[0], 0.8, 0.9, 5).argmax()), 4]
+    st = types.SimpleNamespace(reqs=[r])
+    n = 20000
+    first = torch.zeros(V)
+    second = torch.zeros(V)
+    for _ in range(n):
+        toks = Engine._accept_sampled(eng, st, [draft], logits, [0])[0]
+        first[toks[0]] += 1
+        if toks[0] == draft[0]:
+            second[toks[1]] += 1
+    p0 = sampling_probs(logits[0], 0.8, 0.9, 5)
+    p1 = sampling_probs(logits[1], 0.8, 0.9, 5)
+    tv0 = 0.5 * (first / n - p0 / p0.sum()).abs().sum().item()
+    tv1 = 0.5 * (second / second.sum() - p1 / p1.sum()).abs().sum().item()
+    assert tv0 < 0.02 and tv1 < 0.03, (tv0, tv1)
+    assert eng.stats["spec_proposed"] == 2 * n
