@@ -8,12 +8,19 @@ graph replays the whole forward (all layers, collectives included) plus
 greedy argmax, and the sampled ids come back to the host.  Padded rows use
 the reserved scratch page 0 so they never touch live KV.
 
+Capture verdicts are agreed over the CPU process group (`capture_agreed`):
+a graph is kept only if every rank recorded its own, else every rank drops
+it and runs that forward eagerly, so ranks never split between graph replay
+and eager launches.
+
 Reference parity: decode/verify forwards are captured by SGLang's graph
-runner (absent); the reference adds per-bucket eager graphs (fg.py, ag.py).
+runner (absent); the reference adds per-bucket eager graphs (fg.py, ag.py)
+whose capture failures are agreed over the TP CPU group so every rank falls
+back together (fg.py:1890-1900, ag.py:2309-2320).
 """
 from __future__ import annotations
 
-from typing import Dict, List, Optional
+from typing import Callable, Dict, List, Optional
 
 import torch
 
@@ -22,6 +29,30 @@ from ..models.batch import ForwardBatch
 
 class _Graph:
     pass
+
+
+class GraphCaptureFailed(RuntimeError):
+    """A capture failed on at least one rank; every rank runs eagerly."""
+
+
+def capture_agreed(record: Callable[[], object], group=None, what: str = "graph"):
+    """Run `record()` (one graph capture) and agree on its verdict over the
+    CPU group with MIN.  Returns record()'s result when every rank succeeded;
+    otherwise raises GraphCaptureFailed on every rank.
+
+    A capture records kernels and collectives without executing them, so a
+    rank whose capture failed has run nothing its peers did not: after the
+    agreement all ranks take the same path (replay or eager) and issue the
+    same collectives in the same order.  Warm-up forwards, which do execute
+    collectives, run before this on every rank."""
+    from ..utils import levers
+    try:
+        out, ok, err = record(), 1, ""
+    except Exception as e:      # any local failure is agreed, never raised alone
+        out, ok, err = None, 0, f"{type(e).__name__}: {e}"
+    if levers.agree_min([ok], group)[0]:
+        return out
+    raise GraphCaptureFailed(f"{what} capture failed on a rank" + (f" (here: {err})" if err else ""))
 
 
 class DecodeGraphRunner:
@@ -38,6 +69,7 @@ class DecodeGraphRunner:
         self.graphs: Dict[int, _Graph] = {}
         self.pool = None
         self.enabled = True
+        self.group = getattr(engine.ps, "cpu_group", None)
 
     def can_run(self, n: int) -> bool:
         return self.enabled and n <= self.batch_sizes[-1]
@@ -86,13 +118,16 @@ class DecodeGraphRunner:
                 self.model.forward_tokens(g.fb, g.temp, g.top_p, g.top_k, g.unif)
         torch.cuda.current_stream(self.dev).wait_stream(s)
         torch.cuda.synchronize(self.dev)
-        # keep_graph: the raw graph stays queryable (kernel-node census)
-        g.graph = torch.cuda.CUDAGraph(keep_graph=True)
-        if self.pool is None:
-            self.pool = torch.cuda.graph_pool_handle()
-        with torch.cuda.graph(g.graph, pool=self.pool):
-            g.tokens = self.model.forward_tokens(g.fb, g.temp, g.top_p, g.top_k, g.unif)
-        g.graph.instantiate()
+
+        def record():
+            # keep_graph: the raw graph stays queryable (kernel-node census)
+            g.graph = torch.cuda.CUDAGraph(keep_graph=True)
+            if self.pool is None:
+                self.pool = torch.cuda.graph_pool_handle()
+            with torch.cuda.graph(g.graph, pool=self.pool):
+                g.tokens = self.model.forward_tokens(g.fb, g.temp, g.top_p, g.top_k, g.unif)
+            g.graph.instantiate()
+        capture_agreed(record, self.group, f"decode graph (batch {bs})")
         tr = getattr(self.model, "tracer", None)
         g.trace_names = list(tr.names) if tr is not None and tr.enabled else []
         self.graphs[bs] = g
@@ -167,6 +202,11 @@ class DecodeGraphRunner:
         """Drop the graphs (before destroying the process group)."""
         self.graphs.clear()
         self.pool = None
+
+    def disable(self) -> None:
+        """After a failed (agreed) capture: decode eagerly from now on."""
+        self.release()
+        self.enabled = False
 
 
 def build_verify_batch(seqs: List[dict], k: int, rows: int, page_size: int, max_pages: int) -> ForwardBatch:
@@ -250,11 +290,14 @@ class VerifyGraphRunner:
                 self.model.forward(g.fb).argmax(-1)
         torch.cuda.current_stream(self.dev).wait_stream(s)
         torch.cuda.synchronize(self.dev)
-        g.graph = torch.cuda.CUDAGraph()
-        if self.pool is None:
-            self.pool = torch.cuda.graph_pool_handle()
-        with torch.cuda.graph(g.graph, pool=self.pool):
-            g.tokens = self.model.forward(g.fb).argmax(-1)
+
+        def record():
+            g.graph = torch.cuda.CUDAGraph()
+            if self.pool is None:
+                self.pool = torch.cuda.graph_pool_handle()
+            with torch.cuda.graph(g.graph, pool=self.pool):
+                g.tokens = self.model.forward(g.fb).argmax(-1)
+        capture_agreed(record, getattr(self.eng.ps, "cpu_group", None), f"verify graph (batch {bs})")
         self.graphs[bs] = g
         return g
 
@@ -352,11 +395,14 @@ class ExtendGraphRunner:
                 self.model.forward(g.fb)
         torch.cuda.current_stream(self.dev).wait_stream(s)
         torch.cuda.synchronize(self.dev)
-        g.graph = torch.cuda.CUDAGraph()
-        if self.pool is None:
-            self.pool = torch.cuda.graph_pool_handle()
-        with torch.cuda.graph(g.graph, pool=self.pool):
-            g.logits = self.model.forward(g.fb)
+
+        def record():
+            g.graph = torch.cuda.CUDAGraph()
+            if self.pool is None:
+                self.pool = torch.cuda.graph_pool_handle()
+            with torch.cuda.graph(g.graph, pool=self.pool):
+                g.logits = self.model.forward(g.fb)
+        capture_agreed(record, getattr(self.eng.ps, "cpu_group", None), f"extend graph {key}")
         self.graphs[key] = g
         return g
 

@@ -32,6 +32,7 @@ from ..models.batch import ForwardBatch, build_batch
 from ..models.deepseek import DeepseekModel
 from ..parallel.state import ParallelState, get_state
 from .request import Request, SamplingParams
+from .cuda_graph import GraphCaptureFailed
 from .scheduler import Scheduler, Step
 
 
@@ -127,7 +128,10 @@ class Engine:
         seqs = [{"tokens": ch, "start": st, "pages": r.pages}
                 for r, ch, st in zip(step.reqs, step.chunks, step.starts)]
         if step.kind == "decode" and self.graphs is not None and self.graphs.can_run(len(seqs)):
-            return self.graphs.run(step, seqs)
+            try:
+                return self.graphs.run(step, seqs)
+            except GraphCaptureFailed as e:    # agreed on every rank: eager decode from now on
+                self._graphs_off("decode", e)
         if (step.kind == "prefill" and self.graphs is not None and self.ecfg.extend_graphs and self.mtp is None
                 and self.extend_graphs_ok):
             if self.extend_graphs is None:
@@ -135,11 +139,8 @@ class Engine:
                 self.extend_graphs = ExtendGraphRunner(self, self.graphs.max_pages)
             try:
                 logits = self.extend_graphs.run(seqs)
-            except RuntimeError as e:      # capture failed: eager prefill from now on
-                from ..utils import levers
-                levers.announce("extend-graphs-off", f"extend graphs off ({e}); eager prefill")
-                self.extend_graphs.release()
-                self.extend_graphs, self.extend_graphs_ok = None, False
+            except GraphCaptureFailed as e:    # agreed on every rank: eager prefill from now on
+                self._graphs_off("extend", e)
                 logits = None
             if logits is not None:
                 return self._sample(step, logits)
@@ -169,8 +170,11 @@ class Engine:
         seqs = [] if step is None else [{"tokens": ch, "start": st, "pages": r.pages}
                                         for r, ch, st in zip(step.reqs, step.chunks, step.starts)]
         if not any_prefill and self.graphs is not None and self.graphs.can_run(max_seq):
-            toks = self.graphs.run(step, seqs, bucket=self.graphs._bucket(max_seq))
-            return [] if toks is None else toks
+            try:
+                toks = self.graphs.run(step, seqs, bucket=self.graphs._bucket(max_seq))
+                return [] if toks is None else toks
+            except GraphCaptureFailed as e:    # agreed on every rank: eager decode from now on
+                self._graphs_off("decode", e)
         if step is None:      # idle rank: one dummy token on the scratch page
             seqs = [{"tokens": [0], "start": 0, "pages": [0]}]
         fb = build_batch(seqs, self.ecfg.page_size, device="cpu")
@@ -178,6 +182,21 @@ class Engine:
         fb = self._to_device(fb)
         logits = self.model.forward(fb)
         return [] if step is None else self._sample(step, logits)
+
+    def _graphs_off(self, kind: str, err: Exception) -> None:
+        """A capture of `kind` failed on some rank (the verdict is agreed, so
+        every rank gets here at the same step): drop those graphs and run
+        that kind of forward eagerly from now on."""
+        from ..utils import levers
+        levers.announce(f"{kind}-graphs-off", f"{kind} graphs off ({err}); eager {kind}")
+        if kind == "decode":
+            self.graphs.disable()
+        elif kind == "verify":
+            self.verify_graphs.release()
+            self.verify_graphs, self.verify_graphs_ok = None, False
+        else:
+            self.extend_graphs.release()
+            self.extend_graphs, self.extend_graphs_ok = None, False
 
     def _to_device(self, fb: ForwardBatch) -> ForwardBatch:
         if self.device.type == "cpu":
@@ -299,11 +318,8 @@ class Engine:
             if self.verify_graphs.can_run(len(seqs)):
                 try:
                     pred = self.verify_graphs.run(seqs)
-                except RuntimeError as e:    # capture failed: verify eagerly from now on
-                    from ..utils import levers
-                    levers.announce("verify-graphs-off", f"verify graphs off ({e}); eager verify")
-                    self.verify_graphs.release()
-                    self.verify_graphs, self.verify_graphs_ok = None, False
+                except GraphCaptureFailed as e:    # agreed on every rank: verify eagerly from now on
+                    self._graphs_off("verify", e)
                 else:
                     starts = [i * (1 + k) for i in range(len(seqs))]
                     return self._accept(st, drafts, pred, starts)
