@@ -45,6 +45,13 @@ class GenerateOutput:
     ttft_s: float
     tpot_s: float
     text: Optional[str] = None
+    logprobs: Optional[List[tuple]] = None   # per token: (token, logprob, [(alt, logprob), ...])
+
+
+def _wants_lp(reqs) -> bool:
+    """Any request of the step asked for log-probabilities (those steps run
+    with full logits, not the token-only decode graphs)."""
+    return any(r.params.logprobs is not None for r in reqs)
 
 
 class Engine:
@@ -80,6 +87,7 @@ class Engine:
             from .cuda_graph import DecodeGraphRunner
             self.graphs = DecodeGraphRunner(self)
         self.stats: Dict[str, float] = {"steps": 0, "prefill_tokens": 0, "decode_tokens": 0}
+        self._step_lp: Dict[int, list] = {}
         # DP attention: every rank schedules its own requests; ranks agree
         # each step on the mode and on the per-rank token rows of the MoE
         # exchange (gloo, host only), and an idle rank joins with a dummy.
@@ -127,7 +135,8 @@ class Engine:
     def _forward(self, step: Step) -> List[int]:
         seqs = [{"tokens": ch, "start": st, "pages": r.pages}
                 for r, ch, st in zip(step.reqs, step.chunks, step.starts)]
-        if step.kind == "decode" and self.graphs is not None and self.graphs.can_run(len(seqs)):
+        if (step.kind == "decode" and self.graphs is not None and self.graphs.can_run(len(seqs))
+                and not _wants_lp(step.reqs)):      # the decode graph returns token ids only
             try:
                 return self.graphs.run(step, seqs)
             except GraphCaptureFailed as e:    # agreed on every rank: eager decode from now on
@@ -143,11 +152,14 @@ class Engine:
                 self._graphs_off("extend", e)
                 logits = None
             if logits is not None:
-                return self._sample(step, logits)
+                toks = self._sample(step, logits)
+                self._note_lp(step.reqs, logits, range(len(toks)), [[t] for t in toks], step.sample)
+                return toks
         fb = build_batch(seqs, self.ecfg.page_size, device="cpu")
         fb = self._to_device(fb)
         logits = self.model.forward(fb)
         toks = self._sample(step, logits)
+        self._note_lp(step.reqs, logits, range(len(toks)), [[t] for t in toks], step.sample)
         if self.mtp is not None and step.kind == "prefill":
             self._mtp_prefill(step, toks)
         return toks
@@ -162,14 +174,15 @@ class Engine:
         ntok = 0 if step is None else sum(len(c) for c in step.chunks)
         nseq = 0 if step is None else len(step.reqs)
         prefill = step is not None and step.kind == "prefill"
-        v = torch.tensor([int(prefill), ntok, nseq, int(step is not None)], dtype=torch.int64)
+        lp = step is not None and _wants_lp(step.reqs)
+        v = torch.tensor([int(prefill), ntok, nseq, int(step is not None), int(lp)], dtype=torch.int64)
         dist.all_reduce(v, op=dist.ReduceOp.MAX, group=self.ps.cpu_group)
-        any_prefill, max_tok, max_seq, any_work = (int(x) for x in v)
+        any_prefill, max_tok, max_seq, any_work, any_lp = (int(x) for x in v)
         if not any_work:
             return None
         seqs = [] if step is None else [{"tokens": ch, "start": st, "pages": r.pages}
                                         for r, ch, st in zip(step.reqs, step.chunks, step.starts)]
-        if not any_prefill and self.graphs is not None and self.graphs.can_run(max_seq):
+        if not any_prefill and not any_lp and self.graphs is not None and self.graphs.can_run(max_seq):
             try:
                 toks = self.graphs.run(step, seqs, bucket=self.graphs._bucket(max_seq))
                 return [] if toks is None else toks
@@ -181,7 +194,32 @@ class Engine:
         fb.dp_tmax = max(max_tok, 1)
         fb = self._to_device(fb)
         logits = self.model.forward(fb)
-        return [] if step is None else self._sample(step, logits)
+        if step is None:
+            return []
+        toks = self._sample(step, logits)
+        self._note_lp(step.reqs, logits, range(len(toks)), [[t] for t in toks], step.sample)
+        return toks
+
+    def _note_lp(self, reqs, logits: torch.Tensor, rows, emitted: List[List[int]], sample=None) -> None:
+        """Log-probabilities of this step's emitted tokens for requests that
+        asked for them: token emitted[i][j] was produced from logits row
+        rows[i] + j.  The values are the model's (log-softmax of the raw
+        logits, before temperature / top-k / top-p), with the request's top-n
+        alternatives; they are kept until the tokens are appended."""
+        sel = [(r, int(r0) + j, t) for k, (r, r0, em) in enumerate(zip(reqs, rows, emitted))
+               if r.params.logprobs is not None and (sample is None or sample[k]) for j, t in enumerate(em)]
+        if not sel:
+            return
+        dev = logits.device
+        lp = torch.log_softmax(logits[torch.tensor([i for _, i, _ in sel], device=dev)].float(), -1)
+        chosen = lp.gather(1, torch.tensor([[t] for _, _, t in sel], device=dev))[:, 0].tolist()
+        n = max(r.params.logprobs for r, _, _ in sel)
+        tv, ti = lp.topk(n, -1) if n > 0 else (None, None)
+        tv, ti = (tv.tolist(), ti.tolist()) if n > 0 else (None, None)
+        for k, (r, _, t) in enumerate(sel):
+            m = r.params.logprobs
+            top = list(zip(ti[k][:m], tv[k][:m])) if m > 0 else []
+            self._step_lp.setdefault(r.rid, []).append((int(t), float(chosen[k]), top))
 
     def _graphs_off(self, kind: str, err: Exception) -> None:
         """A capture of `kind` failed on some rank (the verdict is agreed, so
@@ -225,6 +263,7 @@ class Engine:
         """Run one scheduler step; returns requests that finished."""
         st = self.sched.next_step()
         multi = None
+        self._step_lp: Dict[int, list] = {}
         if self.dp:
             toks = self._dp_forward(st)
             if st is None:
@@ -257,8 +296,11 @@ class Engine:
         for r, smp, new in zip(st.reqs, st.sample, multi):
             if not smp:
                 continue
-            for t in new:
+            lps = self._step_lp.get(r.rid)
+            for k, t in enumerate(new):
                 r.output.append(int(t))
+                if lps is not None:
+                    r.logprobs.append(lps[k])
                 r.token_times.append(now)
                 if r.t_first is None:
                     r.t_first = now
@@ -298,6 +340,7 @@ class Engine:
         if self.dp or not st.reqs:
             return None
         sampling = any(r.params.temperature > 0 for r in st.reqs)
+        want_lp = _wants_lp(st.reqs)
         drafts = []
         for r in st.reqs:
             room = r.params.max_tokens - len(r.output) - 1
@@ -310,7 +353,7 @@ class Engine:
         seqs = [{"tokens": ch + d, "start": s, "pages": r.pages}
                 for r, ch, s, d in zip(st.reqs, st.chunks, st.starts, drafts)]
         k = self.ecfg.spec_k
-        if self.graphs is not None and self.verify_graphs_ok and not sampling:
+        if self.graphs is not None and self.verify_graphs_ok and not sampling and not want_lp:
             # fixed (1 + spec_k) rows per request: one captured graph per bucket
             if self.verify_graphs is None:
                 from .cuda_graph import VerifyGraphRunner
@@ -332,9 +375,10 @@ class Engine:
         for d in drafts:
             starts.append(off)
             off += 1 + len(d)
-        if sampling:
-            return self._accept_sampled(st, drafts, logits, starts)
-        return self._accept(st, drafts, pred, starts)
+        out = (self._accept_sampled(st, drafts, logits, starts) if sampling
+               else self._accept(st, drafts, pred, starts))
+        self._note_lp(st.reqs, logits, starts, out)
+        return out
 
     def _accept_sampled(self, st: Step, drafts, logits: torch.Tensor, starts: List[int]) -> List[List[int]]:
         """Speculative sampling with deterministic (n-gram) drafts: draft token
@@ -476,13 +520,15 @@ class Engine:
         fb = build_batch(seqs, self.ecfg.page_size, device="cpu")
         fb.last_idx = torch.arange(fb.num_tokens, dtype=torch.int64)     # logits at every position
         fb = self._to_device(fb)
-        pred = self.model.forward(fb).argmax(-1).tolist()
+        logits = self.model.forward(fb)
+        pred = logits.argmax(-1).tolist()
         H = self.model.last_residual
         starts, off = [], 0
         for d in drafts:
             starts.append(off)
             off += 1 + len(d)
         out = self._accept(st, drafts, pred, starts)
+        self._note_lp(st.reqs, logits, starts, out)
         rows, prev = [], []
         for r, o, s0, n in zip(st.reqs, out, starts, st.starts):
             # token positions n + 1 .. n + len(o) hold the accepted tokens
@@ -527,5 +573,6 @@ class Engine:
             tpot = (r.t_done - r.t_first) / (n - 1) if n > 1 else 0.0
             text = self.tokenizer.decode(r.output) if self.tokenizer is not None else None
             outs.append(GenerateOutput(r.rid, len(r.prompt), list(r.output), r.finish_reason or "length",
-                                       (r.t_first or r.t_arrive) - r.t_arrive, tpot, text))
+                                       (r.t_first or r.t_arrive) - r.t_arrive, tpot, text,
+                                       list(r.logprobs) if r.params.logprobs is not None else None))
         return outs

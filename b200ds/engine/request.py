@@ -17,6 +17,7 @@ class SamplingParams:
     seed: Optional[int] = None
     ignore_eos: bool = False
     stop_token_ids: List[int] = field(default_factory=list)
+    logprobs: Optional[int] = None  # record each output token's log-probability and this many top alternatives
 
 
 @dataclass
@@ -35,6 +36,8 @@ class Request:
     t_first: Optional[float] = None
     t_done: Optional[float] = None
     token_times: List[float] = field(default_factory=list)
+    # per output token (SamplingParams.logprobs set): (token, logprob, [(alt token, logprob), ...])
+    logprobs: List[tuple] = field(default_factory=list)
     gen: Optional[torch.Generator] = None
 
     @property

@@ -1,8 +1,9 @@
 """OpenAI-compatible HTTP server.
 
 Endpoints: POST /v1/completions, POST /v1/chat/completions (both with
-``stream: true`` server-sent events), GET /v1/models, GET /health,
-GET /metrics (Prometheus text).
+``stream: true`` server-sent events, ``n``, ``stop`` strings and token ids,
+``seed``, and log-probabilities: ``logprobs`` / ``top_logprobs``), GET
+/v1/models, GET /health, GET /metrics (Prometheus text).
 
 One engine thread owns the Engine and runs `step()` whenever requests are
 pending; HTTP handlers enqueue requests and await their tokens through
@@ -114,8 +115,9 @@ class EngineWorker:
                 alive = True
                 if len(r.output) > sent:
                     new_toks = r.output[sent:]
+                    lps = r.logprobs[sent:] if r.params.logprobs is not None else None
                     self.subs[rid] = (loop, q, len(r.output), r)
-                    alive = _post(loop, q, ("tokens", new_toks))
+                    alive = _post(loop, q, ("tokens", new_toks, lps))
                 if r.finished:
                     _post(loop, q, ("done", r.finish_reason))
                     self.metrics.finish(r)
@@ -179,11 +181,11 @@ class DPEngineWorker(EngineWorker):
             if eng.sched.has_work:
                 self.metrics.step_time.append(time.perf_counter() - t0)
             for upd in _dp_gather(ps, _dp_updates(self.own)):
-                for gid, toks, fin, reason, r in upd:
+                for gid, toks, fin, reason, r, lps in upd:
                     if gid not in self.subs:     # aborted meanwhile
                         continue
                     loop, q, sent, _ = self.subs[gid]
-                    alive = _post(loop, q, ("tokens", toks)) if toks else True
+                    alive = _post(loop, q, ("tokens", toks, lps)) if toks else True
                     if not alive and not fin:
                         self.cancel(q)
                     if fin:
@@ -214,9 +216,10 @@ def _dp_updates(own) -> list:
     for gid, st in list(own.items()):
         r, sent = st
         toks = r.output[sent:]
+        lps = list(r.logprobs[sent:]) if r.params.logprobs is not None else None
         st[1] = len(r.output)
         if toks or r.finished:
-            out.append((gid, list(toks), r.finished, r.finish_reason, None))
+            out.append((gid, list(toks), r.finished, r.finish_reason, None, lps))
         if r.finished:
             del own[gid]
     return out
@@ -328,7 +331,43 @@ def _stop_scan(text: str, stops: List[str]):
     return cut, hold
 
 
-def _params(body: dict, default_max: int = 16) -> SamplingParams:
+def _logprobs_param(body: dict, chat: bool) -> Optional[int]:
+    """OpenAI: completions take `logprobs` = number of alternatives (0-20);
+    chat takes `logprobs: true` and `top_logprobs` (0-20)."""
+    if chat:
+        if not body.get("logprobs"):
+            return None
+        n = int(body.get("top_logprobs") or 0)
+    else:
+        if body.get("logprobs") is None or body.get("logprobs") is False:
+            return None
+        n = int(body["logprobs"])
+    if not 0 <= n <= 20:
+        raise ValueError("logprobs / top_logprobs must be between 0 and 20")
+    return n
+
+
+def _lp_json(tok, lps, chat: bool, offset: int = 0) -> dict:
+    """Engine log-probabilities -> the OpenAI response field (chat: `content`
+    entries with token, logprob, bytes, top_logprobs; completions: parallel
+    tokens / token_logprobs / top_logprobs / text_offset lists)."""
+    if chat:
+        def ent(t, lp):
+            s = tok.decode([t])
+            return {"token": s, "logprob": lp, "bytes": list(s.encode("utf-8")), "token_id": t}
+        return {"content": [dict(ent(t, lp), top_logprobs=[ent(a, alp) for a, alp in top]) for t, lp, top in lps]}
+    toks, offs = [], []
+    for t, _, _ in lps:
+        s = tok.decode([t])
+        toks.append(s)
+        offs.append(offset)
+        offset += len(s)
+    return {"tokens": toks, "token_logprobs": [lp for _, lp, _ in lps],
+            "top_logprobs": [{tok.decode([a]): alp for a, alp in top} for _, _, top in lps],
+            "text_offset": offs}
+
+
+def _params(body: dict, default_max: int = 16, chat: bool = False) -> SamplingParams:
     stop_ids = body.get("stop_token_ids") or []
     return SamplingParams(
         max_tokens=int(body.get("max_tokens") or default_max),
@@ -338,6 +377,7 @@ def _params(body: dict, default_max: int = 16) -> SamplingParams:
         seed=body.get("seed"),
         ignore_eos=bool(body.get("ignore_eos", False)),
         stop_token_ids=list(stop_ids),
+        logprobs=_logprobs_param(body, chat),
     )
 
 
@@ -374,13 +414,17 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
         """Tokens of one subscription until it finishes (or a stop string
         appears): (token ids, text, finish reason)."""
         out: List[int] = []
+        lps: List[tuple] = []
         reason = "length"
         text = None
         try:
             while True:
-                kind, val = await q.get()
+                ev = await q.get()
+                kind, val = ev[0], ev[1]
                 if kind == "tokens":
                     out.extend(val)
+                    if len(ev) > 2 and ev[2]:
+                        lps.extend(ev[2])
                     if stops:
                         cut, _ = _stop_scan(tok.decode(out), stops)
                         if cut is not None:
@@ -393,12 +437,15 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
         except BaseException:              # cancelled (client gone)
             worker.cancel(q)
             raise
-        return out, (tok.decode(out) if text is None else text), reason
+        return out, (tok.decode(out) if text is None else text), reason, lps
 
     async def _handle(request: Request, chat: bool):
         body = await request.json()
         ids = _prompt_ids(body, chat)
-        params = _params(body)
+        try:
+            params = _params(body, chat=chat)
+        except ValueError as e:
+            raise HTTPException(400, str(e))
         rid = f"{'chatcmpl' if chat else 'cmpl'}-{uuid.uuid4().hex[:16]}"
         created = int(time.time())
         n = int(body.get("n") or 1)
@@ -407,17 +454,21 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
         obj = "chat.completion" if chat else "text_completion"
         stops = body.get("stop") or []
         stops = [stops] if isinstance(stops, str) else [x for x in stops if isinstance(x, str) and x]
+
+        def _choice(i, out, text, reason, lps):
+            c = ({"index": i, "message": {"role": "assistant", "content": text}, "finish_reason": reason} if chat
+                 else {"index": i, "text": text, "token_ids": out, "finish_reason": reason})
+            if params.logprobs is not None:
+                c["logprobs"] = _lp_json(tok, lps, chat)
+            return c
         if n > 1:
             # n independent samples of the prompt (seed + i when a seed is given)
             import dataclasses
             qs = [await _run(ids, dataclasses.replace(params, seed=None if params.seed is None else params.seed + i))
                   for i in range(n)]
             results = [await _collect(q, stops) for q in qs]
-            choices = []
-            for i, (out, text, reason) in enumerate(results):
-                choices.append({"index": i, "message": {"role": "assistant", "content": text}, "finish_reason": reason}
-                               if chat else {"index": i, "text": text, "token_ids": out, "finish_reason": reason})
-            gen_tok = sum(len(o) for o, _, _ in results)
+            choices = [_choice(i, out, text, reason, lps) for i, (out, text, reason, lps) in enumerate(results)]
+            gen_tok = sum(len(o) for o, _, _, _ in results)
             return JSONResponse({"id": rid, "object": obj, "created": created, "model": model_name,
                                  "choices": choices, "usage": {"prompt_tokens": len(ids), "completion_tokens": gen_tok,
                                                                "total_tokens": len(ids) + gen_tok}})
@@ -437,8 +488,12 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
                 ids_all: List[int] = []
                 sent = 0                      # characters of the decoded text already streamed
                 while True:
-                    kind, val = await q.get()
+                    ev = await q.get()
+                    kind, val = ev[0], ev[1]
                     if kind == "tokens":
+                        lp_field = None
+                        if params.logprobs is not None and len(ev) > 2 and ev[2]:
+                            lp_field = _lp_json(tok, ev[2], chat, len(tok.decode(ids_all)))
                         ids_all.extend(val)
                         full = tok.decode(ids_all)
                         cut, hold = _stop_scan(full, stops)
@@ -448,6 +503,8 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
                         if text or cut is None:
                             choice = ({"index": 0, "delta": {"content": text}, "finish_reason": None} if chat
                                       else {"index": 0, "text": text, "token_ids": val, "finish_reason": None})
+                            if lp_field is not None:
+                                choice["logprobs"] = lp_field
                             yield f"data: {json.dumps({'id': rid, 'object': obj + '.chunk', 'created': created, 'model': model_name, 'choices': [choice]})}\n\n"
                         if cut is not None:     # a stop string: finish now and free the request
                             worker.cancel(q)
@@ -463,9 +520,8 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
                         yield "data: [DONE]\n\n"
                         return
             return StreamingResponse(gen(), media_type="text/event-stream")
-        out, text, reason = await _collect(q, stops)
-        choice = ({"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": reason} if chat
-                  else {"index": 0, "text": text, "token_ids": out, "finish_reason": reason})
+        out, text, reason, lps = await _collect(q, stops)
+        choice = _choice(0, out, text, reason, lps)
         return JSONResponse({"id": rid, "object": obj, "created": created, "model": model_name, "choices": [choice],
                              "usage": {"prompt_tokens": len(ids), "completion_tokens": len(out),
                                        "total_tokens": len(ids) + len(out)}})

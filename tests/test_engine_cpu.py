@@ -196,10 +196,39 @@ def test_server_cancel_aborts_request():
     lp = Loop()
     w.submit(list(range(40)), SamplingParams(max_tokens=10000), lp, lp)
     t0 = _t.time()
-    while not any(k == "tokens" for k, _ in lp.items) and _t.time() - t0 < 60:
+    while not any(ev[0] == "tokens" for ev in lp.items) and _t.time() - t0 < 60:
         _t.sleep(0.01)
     w.cancel(lp)
-    while not any(k == "done" for k, _ in lp.items) and _t.time() - t0 < 60:
+    while not any(ev[0] == "done" for ev in lp.items) and _t.time() - t0 < 60:
         _t.sleep(0.01)
     w.stop()
     assert ("done", "abort") in lp.items and not eng.sched.has_work
+
+
+def test_logprobs_match_oracle_and_leave_tokens_unchanged():
+    """SamplingParams.logprobs: every output token carries the model's
+    log-probability (log-softmax of the raw logits) and the top-n
+    alternatives; the values match the fp32 oracle's logits of the prefix,
+    and asking for them does not change the tokens."""
+    from b200ds.models.reference import ReferenceModel, init_weights
+    eng, cfg = _engine(False)
+    g = torch.Generator().manual_seed(8)
+    prompts = torch.randint(0, cfg.vocab_size, (2, 11), generator=g).tolist()
+    plain = [o.token_ids for o in eng.generate(prompts, SamplingParams(max_tokens=5))]
+    outs = eng.generate(prompts, SamplingParams(max_tokens=5, logprobs=3))
+    assert [o.token_ids for o in outs] == plain
+    oracle = ReferenceModel(cfg, init_weights(cfg, 0))
+    for p, o in zip(prompts, outs):
+        assert len(o.logprobs) == len(o.token_ids)
+        seq = torch.tensor([p + o.token_ids])
+        oracle.reset(1)
+        want = torch.log_softmax(oracle.forward(seq, 0)[0].float(), -1)
+        for j, (t, lp, top) in enumerate(o.logprobs):
+            row = want[len(p) - 1 + j]
+            assert t == o.token_ids[j] and abs(lp - float(row[t])) < 1e-3
+            assert [a for a, _ in top] == row.topk(3).indices.tolist()
+            assert top[0][0] == t                       # greedy: the sampled token is the top one
+    none = eng.generate(prompts[:1], SamplingParams(max_tokens=3))[0]
+    assert none.logprobs is None
+    zero = eng.generate(prompts[:1], SamplingParams(max_tokens=3, logprobs=0))[0]
+    assert all(top == [] for _, _, top in zero.logprobs) and len(zero.logprobs) == 3

@@ -79,3 +79,30 @@ def test_n_choices(client):
     again = client.post("/v1/completions", json={"prompt": [3, 4, 5], "max_tokens": 4, "temperature": 0.9,
                                                  "seed": 11, "n": 3}).json()
     assert [c["token_ids"] for c in again["choices"]] == [c["token_ids"] for c in r["choices"]]
+
+
+def test_logprobs_fields(client):
+    """OpenAI log-probability fields: completions (`logprobs: n` -> tokens /
+    token_logprobs / top_logprobs / text_offset), chat (`logprobs: true`,
+    `top_logprobs` -> content entries), and per chunk when streaming."""
+    r = client.post("/v1/completions", json={"prompt": [5, 6, 7], "max_tokens": 4, "temperature": 0,
+                                             "logprobs": 2}).json()
+    c = r["choices"][0]
+    lp = c["logprobs"]
+    assert len(lp["tokens"]) == len(lp["token_logprobs"]) == len(lp["top_logprobs"]) == 4
+    assert all(v <= 0 for v in lp["token_logprobs"]) and all(len(t) <= 2 for t in lp["top_logprobs"])
+    assert lp["text_offset"][0] == 0
+    ch = client.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "hi"}], "max_tokens": 3,
+                                                   "temperature": 0, "logprobs": True, "top_logprobs": 2}).json()
+    content = ch["choices"][0]["logprobs"]["content"]
+    assert len(content) == 3 and all(len(e["top_logprobs"]) == 2 for e in content)
+    assert content[0]["top_logprobs"][0]["token_id"] == content[0]["token_id"]     # greedy
+    plain = client.post("/v1/completions", json={"prompt": [5, 6, 7], "max_tokens": 4, "temperature": 0}).json()
+    assert "logprobs" not in plain["choices"][0] and plain["choices"][0]["token_ids"] == c["token_ids"]
+    with client.stream("POST", "/v1/completions", json={"prompt": [5, 6, 7], "max_tokens": 4, "temperature": 0,
+                                                        "logprobs": 1, "stream": True}) as s:
+        events = [json.loads(l[6:]) for l in s.iter_lines() if l.startswith("data: ") and l != "data: [DONE]"]
+    streamed = sum((e["choices"][0].get("logprobs", {}).get("token_logprobs", []) for e in events), [])
+    assert len(streamed) == 4 and abs(streamed[0] - lp["token_logprobs"][0]) < 1e-5
+    bad = client.post("/v1/completions", json={"prompt": [5], "max_tokens": 1, "logprobs": 50})
+    assert bad.status_code == 400

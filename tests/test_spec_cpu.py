@@ -173,3 +173,30 @@ def test_speculative_sampling_preserves_distribution():
     tv1 = 0.5 * (second / second.sum() - p1 / p1.sum()).abs().sum().item()
     assert tv0 < 0.02 and tv1 < 0.03, (tv0, tv1)
     assert eng.stats["spec_proposed"] == 2 * n
+
+
+def test_logprobs_under_speculative_decoding():
+    """Log-probabilities of tokens accepted from a draft come from the verify
+    forward's row for that position: the same values as plain decoding."""
+    from b200ds import build_model_from
+    from b200ds.config import EngineConfig, tiny_config
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.reference import init_weights
+    cfg = tiny_config()
+    sd = init_weights(cfg, 0)
+    g = torch.Generator().manual_seed(2)
+    base = torch.randint(0, cfg.vocab_size, (6,), generator=g).tolist()
+    prompts = [base * 4]
+
+    def run(spec):
+        ecfg = EngineConfig(page_size=8, cuda_graphs=False, spec_ngram=spec, spec_k=4)
+        eng = Engine(build_model_from(cfg, ecfg, sd, device="cpu"), ecfg)
+        o = eng.generate(prompts, SamplingParams(max_tokens=16, logprobs=2))[0]
+        return o, eng.stats
+    plain, _ = run(0)
+    spec, stats = run(3)
+    assert stats.get("spec_accepted", 0) > 0
+    assert spec.token_ids == plain.token_ids and len(spec.logprobs) == len(plain.logprobs)
+    for a, b in zip(spec.logprobs, plain.logprobs):
+        assert a[0] == b[0] and abs(a[1] - b[1]) < 1e-3 and [t for t, _ in a[2]] == [t for t, _ in b[2]]
