@@ -85,6 +85,10 @@ class DeepseekV4Model:
         self.kv_dtype = kv_dtype
         self.heads = cfg.num_attention_heads // ps.tp_size
         self.groups = cfg.o_groups // ps.tp_size
+        # DP attention: each rank runs attention, mHC, Engram, dense / shared
+        # FFNs and the LM head for its own requests with replicated weights
+        # (tp_size 1); only the routed experts are EP-split
+        self.dp = bool(ecfg.dp_attention) and ps.ep_size > 1
         self.rope_table = cos_sin_table(cfg, cfg.max_position_embeddings, device=self.device)
         self.kv_scale = [1.0] * len(layers)
         self.kv_cache: List[torch.Tensor] = []
@@ -126,6 +130,8 @@ class DeepseekV4Model:
         return torch.float32 if self.device.type == "cpu" else torch.bfloat16
 
     def _reduce(self, y: torch.Tensor) -> torch.Tensor:
+        if self.dp:                 # replicated weights, this rank's own tokens: nothing to sum
+            return y
         if self.ps.tp_size > 1:
             self.ps.tp_all_reduce(y)
         elif self.ps.ep_size > 1:
@@ -168,10 +174,39 @@ class DeepseekV4Model:
         w, ids = ops.router(h, mw.gate, mw.bias, c)
         if fb.is_decode and c.prune_budget > 0:
             w, ids = ops.e5_prune(w, ids, c, c.n_routed_experts)
+        if self.dp:
+            return self._moe_dp(mw, h, w, ids, fb)
         out = ops.moe_experts(h, w, ids, mw.experts, out_dtype=od, n_experts_total=c.n_routed_experts)
         if mw.shared_gate_up is not None:
             out = out + mw.shared_down(ops.gate_up_swiglu(h, mw.shared_gate_up), out_dtype=od)
         return self._reduce(out.to(od))
+
+    def _moe_dp(self, mw: MoEWeights, h, w: torch.Tensor, ids: torch.Tensor, fb: ForwardBatch) -> torch.Tensor:
+        """Routed experts under DP attention.  Each rank has routed (and, in
+        decode, E5-pruned over its own batch) its T_r tokens; tokens, weights
+        and expert ids are all-gathered over the EP group, padded to the
+        step's agreed T_step rows per rank (padding rows carry no expert),
+        every rank runs its local experts over all ranks' rows, the partial
+        sums are all-reduced and each rank keeps its own rows plus its
+        replicated shared expert.  Collectives: NCCL / gloo."""
+        c, ps = self.cfg, self.ps
+        od = self._out_dtype()
+        T_r = fb.num_tokens
+        T_step = max(int(fb.dp_tmax or 0), T_r)
+        x = ops.to_float(h).to(od)
+        w = w.float()
+        if T_step > T_r:
+            pad = T_step - T_r
+            x = torch.cat([x, x.new_zeros(pad, x.shape[1])], 0)
+            w = torch.cat([w, w.new_zeros(pad, w.shape[1])], 0)
+            ids = torch.cat([ids, ids.new_full((pad, ids.shape[1]), -1)], 0)
+        g, gw, gi = ps.ep_all_gather(x.contiguous()), ps.ep_all_gather(w.contiguous()), ps.ep_all_gather(ids.contiguous())
+        part = ops.moe_experts(g, gw, gi, mw.experts, out_dtype=torch.float32, n_experts_total=c.n_routed_experts)
+        ps.ep_all_reduce(part)
+        out = part[ps.ep_rank * T_step: ps.ep_rank * T_step + T_r]
+        if mw.shared_gate_up is not None:
+            out = out + mw.shared_down(ops.gate_up_swiglu(h, mw.shared_gate_up), out_dtype=torch.float32).float()
+        return out.to(od)
 
     def _ffn_first_linear(self, lw: V4LayerWeights):
         if isinstance(lw.ffn, DenseWeights):
@@ -261,7 +296,7 @@ def build_model_v4(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState, sd: 
         k_norm.weight}.
     """
     from .loader import _quantize, build_ffn
-    assert not ecfg.dp_attention, "DeepSeek-V4 family: TP attention + EP experts"
+    assert not ecfg.dp_attention or ps.tp_size == 1, "DP attention replicates the non-expert weights (tp_size 1)"
     dev = torch.device(device)
     tp, tr = ps.tp_size, ps.tp_rank
     H, L, G, R = cfg.num_attention_heads, cfg.kv_lora_rank, cfg.o_groups, cfg.o_lora_rank

@@ -153,3 +153,40 @@ def test_v4_sparse_indexer_with_window_matches_oracle():
     outs = eng.generate(prompts.tolist(), SamplingParams(max_tokens=5))
     oracle = ReferenceV4Model(cfg, sd, 128)
     assert [o.token_ids for o in outs] == oracle.greedy(prompts, 5).tolist()
+
+
+def _dp_rank(rank, world):
+    from b200ds import build_model_from
+    from b200ds.config import EngineConfig, tiny_v4_config
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.reference_v4 import init_weights_v4
+    from b200ds.parallel.state import init_parallel
+    ps = init_parallel(backend="gloo", dp_attention=True)
+    cfg = tiny_v4_config()
+    ecfg = EngineConfig(page_size=8, cuda_graphs=False, enable_prefix_cache=False, max_prefill_tokens=7,
+                        tp_size=1, ep_size=world, dp_attention=True)
+    eng = Engine(build_model_from(cfg, ecfg, init_weights_v4(cfg, 0), device="cpu", ps=ps), ecfg)
+    mine = [i for i in range(3) if i % world == rank]
+    prompts = _prompts(cfg, 3, 11, seed=6)
+    maxt = [7, 4, 9]
+    outs = eng.generate([prompts[i].tolist() for i in mine], [SamplingParams(max_tokens=maxt[i]) for i in mine])
+    return mine, [o.token_ids for o in outs]
+
+
+def test_v4_dp2_ep2_gloo_matches_single():
+    """DP attention for the V4 family: each rank runs attention, mHC, Engram
+    and the head for its own requests with replicated weights; routed
+    experts are EP-split and the MoE exchanges the ranks' rows (uneven
+    ranks: rank 1 idles with dummy rows at the end).  Each rank's tokens
+    equal a single-process run of its own requests (the E5 prune acts on
+    each rank's decode batch)."""
+    from b200ds.engine.request import SamplingParams
+    res = run_ranks(_dp_rank, 2)
+    for mine, toks in res:
+        eng, cfg = _v4_engine(chunk=7)
+        prompts = _prompts(cfg, 3, 11, seed=6)
+        maxt = [7, 4, 9]
+        want = [o.token_ids for o in eng.generate([prompts[i].tolist() for i in mine],
+                                                  [SamplingParams(max_tokens=maxt[i]) for i in mine])]
+        assert toks == want, (mine, toks, want)
