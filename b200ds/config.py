@@ -93,6 +93,11 @@ class ModelConfig:
     engram_clamp: float = 10.0
     # layers whose residual-stream mean is exported (draft-model taps)
     aux_layers: tuple = ()
+    # Window-only late layers: layers >= late_layer_start attend to the last
+    # late_window positions (up to and including the query) and skip the
+    # indexer.  Prefill then needs those layers only on each prompt's tail.
+    late_layer_start: Optional[int] = None
+    late_window: int = 0
 
     # ---- derived -----------------------------------------------------------
     @property
@@ -112,6 +117,22 @@ class ModelConfig:
 
     def is_moe_layer(self, i: int) -> bool:
         return self.n_routed_experts > 0 and i >= self.first_k_dense_replace
+
+    def is_window_layer(self, i: int) -> bool:
+        return self.late_layer_start is not None and self.late_window > 0 and i >= self.late_layer_start
+
+    def tail_rows_needed(self) -> int:
+        """Positions before a prompt's end whose window-layer rows a prefill
+        must compute so that every later read is exact.  A row left out
+        leaves that layer's key row unwritten; a computed row whose window
+        reaches an unwritten one is off, and each further window layer
+        spreads that late_window - 1 rows forward.  With n window layers the
+        last row's output (the logits) and the decode windows' key rows
+        (positions >= end - late_window + 1 in every window layer) stay
+        exact when the rows from end - n * (late_window - 1) - 1 on are
+        computed."""
+        n = self.num_hidden_layers - self.late_layer_start
+        return n * (self.late_window - 1) + 1
 
     @property
     def softmax_scale(self) -> float:
@@ -301,6 +322,7 @@ class EngineConfig:
     max_num_seqs: int = 256          # concurrent running requests
     max_prefill_tokens: int = 16384  # chunked-prefill budget per step
     mixed_steps: bool = False        # prefill steps also advance running requests by one decode token
+    prefill_tail: bool = True        # window-only late layers (V4 family) run only on each prompt's tail rows
     kv_cache_fraction: float = 0.85  # of free HBM after weights
     max_kv_pages: Optional[int] = None
     cuda_graphs: bool = True         # capture decode per batch bucket

@@ -156,6 +156,7 @@ class Engine:
                 self._note_lp(step.reqs, logits, range(len(toks)), [[t] for t in toks], step.sample)
                 return toks
         fb = build_batch(seqs, self.ecfg.page_size, device="cpu")
+        fb.tail_from = self._tail_from(step)
         fb = self._to_device(fb)
         logits = self.model.forward(fb)
         toks = self._sample(step, logits)
@@ -192,6 +193,7 @@ class Engine:
             seqs = [{"tokens": [0], "start": 0, "pages": [0]}]
         fb = build_batch(seqs, self.ecfg.page_size, device="cpu")
         fb.dp_tmax = max(max_tok, 1)
+        fb.tail_from = None if step is None else self._tail_from(step)
         fb = self._to_device(fb)
         logits = self.model.forward(fb)
         if step is None:
@@ -199,6 +201,23 @@ class Engine:
         toks = self._sample(step, logits)
         self._note_lp(step.reqs, logits, range(len(toks)), [[t] for t in toks], step.sample)
         return toks
+
+    def _tail_from(self, step: Step) -> Optional[torch.Tensor]:
+        """Prefill tail of a step (window-only late layers, V4 family): per
+        sequence, the first position those layers must compute - a prompt
+        needs only its last `tail_rows_needed()` positions there, a decode
+        row in a mixed step needs its row.  None when off: no window layers,
+        EngineConfig.prefill_tail off, or the prefix cache / MTP draft on
+        (both reuse rows a tail would leave out)."""
+        c = self.model.cfg
+        if (step.kind != "prefill" or not c.is_v4 or c.late_layer_start is None or c.late_window <= 0
+                or not self.ecfg.prefill_tail or self.radix is not None or self.mtp is not None):
+            return None
+        from .scheduler import prefill_target
+        n_pre = len(step.reqs) - step.decode_rows
+        need = c.tail_rows_needed()
+        return torch.tensor([max(0, prefill_target(r) - need) if k < n_pre else 0
+                             for k, r in enumerate(step.reqs)], dtype=torch.int32)
 
     def _note_lp(self, reqs, logits: torch.Tensor, rows, emitted: List[List[int]], sample=None) -> None:
         """Log-probabilities of this step's emitted tokens for requests that

@@ -32,6 +32,9 @@ class ForwardBatch:
     temperature: Optional[torch.Tensor] = None
     top_p: Optional[torch.Tensor] = None
     top_k: Optional[torch.Tensor] = None
+    # Prefill tail [B]: window-only late layers compute only the rows at
+    # positions >= tail_from[sequence] (and each sequence's last row)
+    tail_from: Optional[torch.Tensor] = None
 
     @property
     def num_tokens(self) -> int:
@@ -40,6 +43,22 @@ class ForwardBatch:
     @property
     def batch_size(self) -> int:
         return int(self.seq_lens.shape[0])
+
+    def tail_rows(self) -> torch.Tensor:
+        """Indices of the rows the window-only late layers compute."""
+        keep = self.positions.long() >= self.tail_from.to(self.positions.device).long()[self.q_seq.long()]
+        keep[self.last_idx.long()] = True
+        return keep.nonzero().flatten()
+
+    def take_rows(self, rows: torch.Tensor) -> "ForwardBatch":
+        """The same sequences with only token rows `rows` (ascending, each
+        sequence's last row included): per-sequence metadata is unchanged,
+        last_idx points into the kept rows."""
+        last = torch.searchsorted(rows, self.last_idx.to(rows.device).long())
+        kw = dict(self.__dict__)
+        kw.update(input_ids=self.input_ids[rows], positions=self.positions[rows], q_seq=self.q_seq[rows],
+                  out_slots=self.out_slots[rows], last_idx=last.to(self.last_idx.dtype), tail_from=None)
+        return ForwardBatch(**kw)
 
     def to(self, device) -> "ForwardBatch":
         kw = {}

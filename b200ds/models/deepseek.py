@@ -129,6 +129,7 @@ class DeepseekModel:
         # attention / dense / shared-expert / LM-head weights (tp_size 1);
         # only the routed experts are split (EP) and exchanged at the MoE
         # boundary.  ps_local is the single-rank view for local reductions.
+        assert cfg.late_layer_start is None, "window-only late layers are a DeepSeek-V4-family option"
         self.dp = bool(ecfg.dp_attention) and ps.ep_size > 1
         self.ps_local = ParallelState(device=self.device) if self.dp else ps
         from ..utils import levers

@@ -95,6 +95,7 @@ class DeepseekV4Model:
         self.tok_cache: Optional[torch.Tensor] = None
         self.page_size = ecfg.page_size
         self.aux: List[torch.Tensor] = []
+        self.tail_skipped = 0            # rows the last prefill tail left out of the window layers
         from ..utils.trace import null_tracer
         self.tracer = null_tracer()
         from ..ops.ref import engram_multipliers
@@ -151,7 +152,13 @@ class DeepseekV4Model:
         qo = aw.wq_b(q_lat, out_dtype=od)
         q = qo[:, : self.heads * L].view(T, self.heads, L)
         topk = None
-        if c.index_n_heads:
+        if c.is_window_layer(i):
+            # window-only layer: the selection is the last late_window positions
+            # (built on the device from the positions, graph-safe)
+            W = c.late_window
+            topk = fb.positions.view(-1, 1).to(torch.int32) - torch.arange(W, dtype=torch.int32, device=fb.positions.device)
+            topk = torch.where(topk >= 0, topk, torch.full_like(topk, -1))
+        elif c.index_n_heads:
             nh, hd = c.index_n_heads, c.index_head_dim
             base = ql + L
             ops.index_k_store(qkv[:, base: base + hd], aw.ix_k_norm_w, aw.ix_k_norm_b, 1e-6, self.rope_table,
@@ -214,6 +221,9 @@ class DeepseekV4Model:
         return lw.ffn.shared_gate_up
 
     def _hidden(self, fb: ForwardBatch):
+        """All layers + the head combine; returns (normed hidden, batch) where
+        the batch is the prefill tail's when window-only late layers ran on
+        a subset of the rows."""
         c = self.cfg
         eps = c.rms_norm_eps
         tr = self.tracer
@@ -224,11 +234,20 @@ class DeepseekV4Model:
         if c.engram_layers:
             eids = ops.engram_ids(fb, self.tok_cache, c, self.engram_mults, self.page_size)
         self.aux = []
+        self.tail_skipped = 0
         carry = None
         for i, lw in enumerate(self.layers):
             tr.mark(f"L{i}.attn")
             if carry is not None:
                 ss = ops.hc_post(X, *carry)
+            if i == c.late_layer_start and fb.tail_from is not None:
+                # prefill tail: the window-only layers need only the rows within
+                # reach of each prompt's end (ForwardBatch.tail_rows)
+                rows = fb.tail_rows()
+                self.tail_skipped = fb.num_tokens - int(rows.numel())
+                X, ss = X[rows].contiguous(), ss[rows].contiguous()
+                eids = eids[rows].contiguous() if eids is not None else None
+                fb = fb.take_rows(rows)
             if lw.engram is not None:
                 ss = ops.engram_update(X, eids, lw.engram, c, self.ps)
             if i in c.aux_layers:
@@ -244,7 +263,7 @@ class DeepseekV4Model:
         tr.mark("head")
         ss = ops.hc_post(X, *carry)
         h, _, _ = ops.hc_pre(X, ss, self.hc_head, self.final_ln, eps, c, None, head=True)
-        return h
+        return h, fb
 
     def _last_hidden(self, h, fb: ForwardBatch) -> torch.Tensor:
         x = ops.to_float(h)
@@ -257,12 +276,12 @@ class DeepseekV4Model:
     @torch.no_grad()
     def forward(self, fb: ForwardBatch) -> torch.Tensor:
         """Logits [B, V] (full vocab) of each sequence's last token."""
-        h = self._hidden(fb)
+        h, fb = self._hidden(fb)
         return ops.lm_head_logits(self._last_hidden(h, fb), self.lm_head, self.ps)
 
     @torch.no_grad()
     def forward_tokens(self, fb: ForwardBatch, temperature, top_p, top_k, uniform) -> torch.Tensor:
-        h = self._hidden(fb)
+        h, fb = self._hidden(fb)
         local = ops.lm_head_local(self._last_hidden(h, fb), self.lm_head)
         out = ops.sample_tokens(local, self.vocab_offset(), temperature, top_p, top_k, uniform, self.ps)
         self.tracer.mark("end")

@@ -182,7 +182,10 @@ class ReferenceV4Model:
         s = torch.einsum("bshd,bld->bhsl", q, keys) * c.softmax_scale
         causal = torch.arange(end).view(1, end) <= (start + torch.arange(S)).view(S, 1)
         mask = causal.view(1, 1, S, end)
-        if c.index_n_heads:
+        if c.is_window_layer(i):          # window-only late layer: the last late_window positions
+            win = torch.arange(end).view(1, end) > (start + torch.arange(S)).view(S, 1) - c.late_window
+            mask = mask & win.view(1, 1, S, end)
+        elif c.index_n_heads:
             mask = mask & self._indexer_select(i, x, qr, pos, start, S).unsqueeze(1)
         s = s.masked_fill(~mask, float("-inf"))
         if c.attn_sink:

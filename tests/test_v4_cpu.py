@@ -190,3 +190,38 @@ def test_v4_dp2_ep2_gloo_matches_single():
         want = [o.token_ids for o in eng.generate([prompts[i].tolist() for i in mine],
                                                   [SamplingParams(max_tokens=maxt[i]) for i in mine])]
         assert toks == want, (mine, toks, want)
+
+
+def test_v4_window_late_layers_prefill_tail_matches_oracle():
+    """Window-only late layers (layers >= late_layer_start attend to the last
+    late_window positions, no indexer) with the prefill tail: under chunked
+    prefill those layers compute only the rows within reach of each prompt's
+    end (whole early chunks skipped there), and the greedy tokens still
+    equal the fp32 oracle's, which computes every row; the same holds with
+    the tail off and with the prefix cache on (tail off automatically)."""
+    from b200ds import build_model_from
+    from b200ds.config import EngineConfig, tiny_v4_config
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.reference_v4 import ReferenceV4Model, init_weights_v4
+    cfg = tiny_v4_config(late_layer_start=1, late_window=4, index_n_heads=4, index_head_dim=32, index_topk=5,
+                         index_swa=2)
+    sd = init_weights_v4(cfg, 0)
+    prompts = _prompts(cfg, 2, 30, seed=9)
+    want = ReferenceV4Model(cfg, sd, 256).greedy(prompts, 6).tolist()
+    assert cfg.tail_rows_needed() == 7
+
+    def run(**kw):
+        ecfg = EngineConfig(page_size=8, cuda_graphs=False, max_prefill_tokens=7, **kw)
+        m = build_model_from(cfg, ecfg, sd, device="cpu")
+        skipped = []
+        orig = m.forward
+        m.forward = lambda fb: (lambda out: skipped.append(m.tail_skipped) or out)(orig(fb))
+        toks = [o.token_ids for o in Engine(m, ecfg).generate(prompts.tolist(), SamplingParams(max_tokens=6))]
+        return toks, sum(skipped)
+    toks, skipped = run(enable_prefix_cache=False)
+    assert toks == want and skipped > 0
+    toks, skipped = run(enable_prefix_cache=False, prefill_tail=False)
+    assert toks == want and skipped == 0
+    toks, skipped = run(enable_prefix_cache=True)
+    assert toks == want and skipped == 0
