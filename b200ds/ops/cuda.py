@@ -23,6 +23,14 @@ except ImportError as e:  # pragma: no cover - only on a box without the build
 
 from .. import _C
 
+levers.register("srcpin", "B200_SRCPIN", True,
+                "refuse a native library built from other csrc/ sources than the tree's (source-hash pin)")
+if levers.on("srcpin"):
+    from ..utils.srcpin import check_pin
+    _stale = check_pin()
+    if _stale is not None:
+        raise ImportError(f"b200ds native extension: {_stale}")
+
 
 def _qact():
     from . import QAct
