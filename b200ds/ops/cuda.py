@@ -13,6 +13,7 @@ import torch
 import torch.distributed as dist
 
 from ..utils import levers
+from . import tactics
 from .quant import MXFP8Tensor, round_up
 
 try:
@@ -133,14 +134,13 @@ def choose_splits(T: int, N: int, K: int, max_ctas: int = 2 * 148) -> int:
     k-tiles.  (o_proj at N = 7168: 4 splits, 224 CTAs; at 2 splits only 112
     SMs streamed weights, 0.47 of copy bandwidth under ncu.)  max_ctas caps
     the grid (the push epilogue's GEMM keeps its 1.5-wave cap)."""
-    if T > 128:
-        return 1
-    tiles = N // 128
-    ktiles = K // 128
     s = 1
-    while s < 8 and tiles * s * 2 <= max_ctas and ktiles // (s * 2) >= 2:
-        s *= 2
-    return s
+    if T <= 128:
+        tiles = N // 128
+        ktiles = K // 128
+        while s < 8 and tiles * s * 2 <= max_ctas and ktiles // (s * 2) >= 2:
+            s *= 2
+    return tactics.pick("gemm_splits", s, N=N, K=K, rows=T, max_ctas=max_ctas)
 
 
 def gemm(a, w: MXFP8Tensor, out_dtype=torch.bfloat16) -> torch.Tensor:
@@ -215,7 +215,8 @@ def mla_splits(T: int, H: int, max_len: int) -> int:
     groups = H // mla_hb(H)
     ctas = T * max(1, groups)
     tiles = max(1, -(-max_len // 128))
-    return max(1, min(16, 148 // max(ctas, 1), tiles // 2))
+    s = max(1, min(16, 148 // max(ctas, 1), tiles // 2))
+    return tactics.pick("mla_splits", s, H=H, rows=T, keys=max_len)
 
 
 def quant_heads(y: torch.Tensor):
@@ -335,10 +336,12 @@ def router(x: torch.Tensor, gate: torch.Tensor, bias: torch.Tensor, cfg):
 
 def moe_tile_n(rows_per_expert: float, cap: int) -> int:
     """Token tile of the grouped GEMMs from the expected rows per expert."""
-    for bn in (16, 32, 64, 128):
-        if rows_per_expert * 1.5 <= bn or bn == cap:
-            return bn
-    return cap
+    bn = cap
+    for b in (16, 32, 64, 128):
+        if rows_per_expert * 1.5 <= b or b == cap:
+            bn = b
+            break
+    return tactics.pick("moe_tile", bn, cap=cap, rows_per_expert=rows_per_expert)
 
 
 def _fused(bn1: int, bn2: int) -> bool:

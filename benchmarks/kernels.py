@@ -210,6 +210,7 @@ def run_mla(B: int, ctx: int, H: int, iters: int, topk: int = 0):
     report("mla_sparse" if topk else "mla_decode", f"B={B} ctx={ctx} H={H}" + (f" top{topk}" if topk else ""), t,
            nbytes=nbytes, flops=flops, flop_peak=2 * BF16,
            note=f"splits={cuda.mla_splits(B, H, keys)} hb={cuda.mla_hb(H)} incl. q quant + merge")
+    return t
 
 
 def mla_sweep(B: int, ctx: int, H: int, iters: int):
@@ -332,16 +333,65 @@ def run_v4(T: int, iters: int, D: int = 5120, H: int = 64, ctx: int = 1040):
     report("v4_e5_prune", f"T={T} top6 of 384", t, note="includes two input copies")
 
 
+# ---------------------------------------------------------------------------
+# tactic tuning: measure every legal choice per decode shape, write a table
+# (b200ds/ops/tactics.py) that B200_TACTICS=<file> loads
+TUNE_GEMMS = [  # DeepSeek-V3 671B decode GEMMs (N, K) at TP1 and TP8 widths
+    ("qkv_a", 2176, 7168), ("q_b", 24576, 1536), ("q_b_tp8", 3072, 1536), ("o_proj", 7168, 16384),
+    ("o_proj_tp8", 7168, 2048), ("shared_gate_up", 4096, 7168), ("shared_down", 7168, 2048),
+    ("dense_down_tp8", 7168, 2304)]
+TUNE_ROWS = (1, 8, 16, 32, 64, 128)
+
+
+def tune(path: str, iters: int) -> None:
+    from b200ds.ops import QAct, cuda, tactics
+    dev = torch.device("cuda")
+    table = {"gemm_splits": [], "mla_splits": []}
+    for name, N, K in TUNE_GEMMS:
+        w = _mx((), N, K, dev)
+        for T in TUNE_ROWS:
+            x = cuda.quant(torch.randn(T, K, device=dev).to(torch.bfloat16))
+            tactics.set_table({})
+            default = cuda.choose_splits(T, N, K)
+            times = {}
+            for s in (1, 2, 4, 8):
+                if not tactics._LEGAL["gemm_splits"](s, dict(N=N, K=K, rows=T, max_ctas=2 * 148)):
+                    continue
+                tactics.set_table({"gemm_splits": [{"N": N, "K": K, "rows": T, "value": s}]})
+                times[s] = timed(lambda: cuda.gemm(QAct(x.q, x.sf), w), iters)
+            best = min(times, key=times.get)
+            table["gemm_splits"].append({"N": N, "K": K, "rows": T, "value": best})
+            print(json.dumps({"tune": f"gemm_{name}", "T": T, "default": default, "best": best,
+                              "us": {str(k): round(v * 1e6, 2) for k, v in times.items()}}), flush=True)
+    for H in (16, 128):
+        for B in (8, 64):
+            times = {}
+            for s in (1, 2, 3, 4, 6, 8):
+                tactics.set_table({"mla_splits": [{"H": H, "rows": B, "keys": [0, 2048], "value": s}]})
+                times[s] = run_mla(B, 1040, H, iters)
+            best = min(times, key=times.get)
+            table["mla_splits"].append({"H": H, "rows": B, "keys": [0, 2048], "value": best})
+            print(json.dumps({"tune": "mla_decode", "H": H, "B": B, "best": best,
+                              "us": {str(k): round(v * 1e6, 2) for k, v in times.items()}}), flush=True)
+    tactics.set_table(None)
+    tactics.write(table, path)
+    print(json.dumps({"tactics_table": path, "entries": sum(len(v) for v in table.values())}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--small", action="store_true", help="reduced sizes (ncu captures)")
+    ap.add_argument("--tune", default="", help="measure the legal tactics and write this tactics table (JSON)")
     a = ap.parse_args()
     import b200ds._C  # noqa: F401
     from b200ds import ops
     ops.set_impl("native")
     torch.cuda.set_device(0)
+    if a.tune:
+        tune(a.tune, a.iters)
+        return
     small = a.small
     cases = [
         # grouped MoE at the headline decode step: 64 tokens x top-8 over 256 experts
