@@ -35,10 +35,15 @@ from ..engine.request import SamplingParams
 class EngineWorker:
     """Runs Engine.step() on a background thread; thread-safe submission."""
 
-    def __init__(self, engine, tokenizer, ps=None):
+    def __init__(self, engine, tokenizer, ps=None, watchdog_s: float = 0.0, watchdog_exit: bool = False):
         self.engine = engine
         self.tok = tokenizer
         self.ps = ps
+        self.error: Optional[str] = None          # set when a step raised: the worker stops serving
+        self.watchdog = None
+        if watchdog_s > 0:
+            from ..utils.watchdog import Watchdog
+            self.watchdog = Watchdog(watchdog_s, exit_code=70 if watchdog_exit else None)
         self.inbox: "queue.Queue" = queue.Queue()
         self.cancels: "queue.Queue" = queue.Queue()     # subscription queues whose client went away
         self.subs: Dict[int, tuple] = {}     # rid -> (loop, asyncio.Queue, emitted count)
@@ -53,9 +58,47 @@ class EngineWorker:
     def stop(self):
         self._stop.set()
         self.t.join(timeout=10)
+        if self.watchdog is not None:
+            self.watchdog.stop()
+
+    def healthy(self) -> bool:
+        return self.error is None and not (self.watchdog is not None and self.watchdog.stalled)
+
+    def health(self) -> dict:
+        if self.error is not None:
+            return {"status": "error", "error": self.error}
+        if self.watchdog is not None and self.watchdog.stalled:
+            return {"status": "stalled", "error": f"engine step over {self.watchdog.timeout_s:.0f} s"}
+        return {"status": "ok"}
 
     def submit(self, prompt_ids: List[int], params: SamplingParams, loop, q) -> None:
+        if self.error is not None:
+            _post(loop, q, ("error", self.error))
+            return
         self.inbox.put((prompt_ids, params, loop, q))
+
+    def _step(self):
+        """One engine step under the watchdog (when configured)."""
+        if self.watchdog is None:
+            return self.engine.step()
+        with self.watchdog.guard():
+            return self.engine.step()
+
+    def _run(self):
+        try:
+            self._loop()
+        except Exception as e:        # the engine failed: fail every request now instead of leaving it hanging
+            import traceback
+            traceback.print_exc()
+            self._fail(f"{type(e).__name__}: {e}")
+
+    def _fail(self, msg: str) -> None:
+        self.error = msg
+        for loop, q, *_ in list(self.subs.values()):
+            _post(loop, q, ("error", msg))
+        self.subs.clear()
+        for _, _, loop, q in self._admit():
+            _post(loop, q, ("error", msg))
 
     def cancel(self, q) -> None:
         """The client of subscription q is gone: abort its request."""
@@ -89,7 +132,7 @@ class EngineWorker:
                 break
         return new
 
-    def _run(self):
+    def _loop(self):
         eng = self.engine
         while not self._stop.is_set():
             new = self._admit()
@@ -109,7 +152,7 @@ class EngineWorker:
                 time.sleep(0.002)
                 continue
             t0 = time.perf_counter()
-            done = eng.step()
+            self._step()
             self.metrics.step_time.append(time.perf_counter() - t0)
             for rid, (loop, q, sent, r) in list(self.subs.items()):
                 alive = True
@@ -152,12 +195,12 @@ class DPEngineWorker(EngineWorker):
     ranks' new tokens are gathered to rank 0, which streams them out.
     Stopping broadcasts a sentinel that ends the followers' loops."""
 
-    def __init__(self, engine, tokenizer, ps):
-        super().__init__(engine, tokenizer, ps)
+    def __init__(self, engine, tokenizer, ps, **kw):
+        super().__init__(engine, tokenizer, ps, **kw)
         self.next_gid = 0
         self.own: Dict[int, list] = {}      # gid -> [request, tokens sent]
 
-    def _run(self):
+    def _loop(self):
         eng, ps = self.engine, self.ps
         world = ps.world_size
         while not self._stop.is_set():
@@ -177,7 +220,7 @@ class DPEngineWorker(EngineWorker):
                 loop, q, _, _ = self.subs.pop(gid)
                 _post(loop, q, ("done", "abort"))
             t0 = time.perf_counter()
-            eng.step()
+            self._step()
             if eng.sched.has_work:
                 self.metrics.step_time.append(time.perf_counter() - t0)
             for upd in _dp_gather(ps, _dp_updates(self.own)):
@@ -421,6 +464,8 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
             while True:
                 ev = await q.get()
                 kind, val = ev[0], ev[1]
+                if kind == "error":
+                    raise HTTPException(500, f"engine error: {val}")
                 if kind == "tokens":
                     out.extend(val)
                     if len(ev) > 2 and ev[2]:
@@ -434,12 +479,16 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
                 else:
                     reason = val
                     break
+        except HTTPException:
+            raise
         except BaseException:              # cancelled (client gone)
             worker.cancel(q)
             raise
         return out, (tok.decode(out) if text is None else text), reason, lps
 
     async def _handle(request: Request, chat: bool):
+        if not worker.healthy():
+            raise HTTPException(503, f"engine unavailable: {worker.health().get('error')}")
         body = await request.json()
         ids = _prompt_ids(body, chat)
         try:
@@ -490,6 +539,10 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
                 while True:
                     ev = await q.get()
                     kind, val = ev[0], ev[1]
+                    if kind == "error":
+                        yield f"data: {json.dumps({'error': {'message': f'engine error: {val}', 'type': 'server_error'}})}\n\n"
+                        yield "data: [DONE]\n\n"
+                        return
                     if kind == "tokens":
                         lp_field = None
                         if params.logprobs is not None and len(ev) > 2 and ev[2]:
@@ -540,7 +593,8 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
 
     @app.get("/health")
     async def health():
-        return {"status": "ok"}
+        h = worker.health()
+        return h if h["status"] == "ok" else JSONResponse(h, status_code=503)
 
     @app.get("/metrics")
     async def metrics():
@@ -567,6 +621,9 @@ def main(argv=None):
     ap.add_argument("--trace", action="store_true", help="device timestamps per layer phase")
     ap.add_argument("--mixed-steps", action="store_true", help="decode tokens ride along with prefill chunks")
     ap.add_argument("--extend-graphs", action="store_true", help="replay prefill chunks from CUDA graphs")
+    ap.add_argument("--watchdog-timeout", type=float, default=300.0,
+                    help="seconds one engine step may run before /health reports a stall (0: off)")
+    ap.add_argument("--watchdog-exit", action="store_true", help="exit the process when the watchdog fires")
     args = ap.parse_args(argv)
     import uvicorn
     from .. import load_engine
@@ -587,7 +644,8 @@ def main(argv=None):
     if ps.rank != 0:
         follower_loop(eng, ps)
         return
-    worker = (DPEngineWorker(eng, tok, ps) if eng.dp else EngineWorker(eng, tok, ps)).start()
+    wd = dict(watchdog_s=args.watchdog_timeout, watchdog_exit=args.watchdog_exit)
+    worker = (DPEngineWorker(eng, tok, ps, **wd) if eng.dp else EngineWorker(eng, tok, ps, **wd)).start()
     uvicorn.run(create_app(worker, model_name=str(args.model)), host=args.host, port=args.port, log_level="warning")
 
 

@@ -106,3 +106,107 @@ def test_logprobs_fields(client):
     assert len(streamed) == 4 and abs(streamed[0] - lp["token_logprobs"][0]) < 1e-5
     bad = client.post("/v1/completions", json={"prompt": [5], "max_tokens": 1, "logprobs": 50})
     assert bad.status_code == 400
+
+
+def _fresh_client(**kw):
+    from fastapi.testclient import TestClient
+    from b200ds import EngineConfig, load_engine
+    from b200ds.engine.tokenizer import ByteTokenizer
+    from b200ds.server.openai import EngineWorker, create_app
+    eng = load_engine("tiny", ecfg=EngineConfig(page_size=8, cuda_graphs=False), device="cpu")
+    tok = ByteTokenizer()
+    eng.tokenizer = tok
+    worker = EngineWorker(eng, tok, **kw)
+    return eng, worker, TestClient(create_app(worker, "tiny"))
+
+
+def test_engine_failure_fails_requests_and_health():
+    """A step that raises fails every pending request (500, or an error event
+    when streaming) instead of leaving it waiting; /health turns 503 and new
+    requests are refused."""
+    eng, worker, client = _fresh_client()
+    calls = {"n": 0}
+    orig = eng.step
+
+    def flaky():
+        calls["n"] += 1
+        if calls["n"] == 3:
+            raise RuntimeError("injected step failure")
+        return orig()
+    eng.step = flaky
+    worker.start()
+    with client as c:
+        assert c.get("/health").json() == {"status": "ok"}
+        r = c.post("/v1/completions", json={"prompt": [1, 2, 3], "max_tokens": 8, "temperature": 0})
+        assert r.status_code == 500 and "injected step failure" in r.json()["detail"]
+        h = c.get("/health")
+        assert h.status_code == 503 and "injected" in h.json()["error"]
+        assert c.post("/v1/completions", json={"prompt": [1], "max_tokens": 2}).status_code == 503
+    worker.stop()
+
+
+def test_watchdog_marks_a_long_step_stalled():
+    """A step running past the watchdog limit turns /health 503 ("stalled")
+    while it runs (stacks dumped once); the server recovers when it ends."""
+    import threading
+    import time
+    from b200ds.utils.watchdog import Watchdog
+    fired = []
+    wd = Watchdog(0.1, on_expire=fired.append, dump=False)
+    with wd.guard():
+        time.sleep(0.4)
+        assert wd.stalled
+    assert not wd.stalled and len(fired) == 1 and fired[0] >= 0.1
+    with wd.guard():
+        pass
+    time.sleep(0.2)
+    assert len(fired) == 1
+    wd.stop()
+
+    eng, worker, client = _fresh_client(watchdog_s=0.2)
+    worker.watchdog.dump = False
+    gate = threading.Event()
+    orig = eng.step
+
+    def slow():
+        gate.wait(5)
+        return orig()
+    eng.step = slow
+    worker.start()
+    with client as c:
+        res = {}
+        t = threading.Thread(target=lambda: res.update(r=c.post("/v1/completions", json={
+            "prompt": [4, 5], "max_tokens": 2, "temperature": 0})))
+        t.start()
+        deadline = time.time() + 5
+        while c.get("/health").status_code == 200 and time.time() < deadline:
+            time.sleep(0.05)
+        h = c.get("/health")
+        assert h.status_code == 503 and h.json()["status"] == "stalled"
+        gate.set()
+        t.join(10)
+        assert res["r"].status_code == 200
+        assert c.get("/health").status_code == 200
+    worker.stop()
+
+
+def test_engine_failure_while_streaming():
+    eng, worker, client = _fresh_client()
+    calls = {"n": 0}
+    orig = eng.step
+
+    def flaky():
+        calls["n"] += 1
+        if calls["n"] == 3:
+            raise RuntimeError("injected step failure")
+        return orig()
+    eng.step = flaky
+    worker.start()
+    with client as c:
+        with c.stream("POST", "/v1/completions", json={"prompt": [1, 2, 3], "max_tokens": 8, "temperature": 0,
+                                                       "stream": True}) as s:
+            lines = [l for l in s.iter_lines() if l.startswith("data: ")]
+        assert lines[-1] == "data: [DONE]"
+        err = json.loads(lines[-2][6:])
+        assert "injected step failure" in err["error"]["message"]
+    worker.stop()
