@@ -33,6 +33,7 @@ from ..models.deepseek import DeepseekModel
 from ..parallel.state import ParallelState, get_state
 from .request import Request, SamplingParams
 from .cuda_graph import GraphCaptureFailed
+from .penalties import adjust_logits, needs_adjust
 from .scheduler import Scheduler, Step
 
 
@@ -49,9 +50,10 @@ class GenerateOutput:
 
 
 def _wants_lp(reqs) -> bool:
-    """Any request of the step asked for log-probabilities (those steps run
-    with full logits, not the token-only decode graphs)."""
-    return any(r.params.logprobs is not None for r in reqs)
+    """Any request of the step asked for log-probabilities or logit
+    adjustments (those steps run with full logits, not the token-only decode
+    graphs)."""
+    return any(r.params.logprobs is not None or needs_adjust(r.params) for r in reqs)
 
 
 class Engine:
@@ -267,6 +269,8 @@ class Engine:
         return ForwardBatch(**kw)
 
     def _sample(self, step: Step, logits: torch.Tensor) -> List[int]:
+        if any(needs_adjust(r.params) for r in step.reqs):
+            logits = adjust_logits(logits, step.reqs, step.sample, self.eos)
         B = logits.shape[0]
         temp = torch.tensor([r.params.temperature for r in step.reqs], dtype=torch.float32)
         if bool((temp <= 0).all()):
@@ -356,8 +360,8 @@ class Engine:
         (logits at every position).  Returns the accepted tokens per request
         (accepted draft prefix + the model's next token), or None when no
         request has a draft (plain decode then)."""
-        if self.dp or not st.reqs:
-            return None
+        if self.dp or not st.reqs or any(needs_adjust(r.params) for r in st.reqs):
+            return None       # drafts are verified against raw logits; adjusted requests decode one token
         sampling = any(r.params.temperature > 0 for r in st.reqs)
         want_lp = _wants_lp(st.reqs)
         drafts = []
@@ -523,7 +527,7 @@ class Engine:
         """Verify the MTP drafts (greedy) in one main-model forward with logits
         and hidden states at every row, then run the MTP module over the
         accepted tokens for the next drafts."""
-        if any(r.params.temperature > 0 for r in st.reqs):
+        if any(r.params.temperature > 0 or needs_adjust(r.params) for r in st.reqs):
             for r in st.reqs:
                 r.mtp_drafts = []
             return None

@@ -18,6 +18,11 @@ class SamplingParams:
     ignore_eos: bool = False
     stop_token_ids: List[int] = field(default_factory=list)
     logprobs: Optional[int] = None  # record each output token's log-probability and this many top alternatives
+    presence_penalty: float = 0.0   # output tokens seen at least once lose this much logit
+    frequency_penalty: float = 0.0  # ... and this much per occurrence
+    repetition_penalty: float = 1.0  # prompt / output tokens: positive logits / r, negative * r
+    min_p: float = 0.0              # drop tokens below min_p x the top probability (temperature > 0)
+    min_tokens: int = 0             # no end-of-sequence / stop token before this many output tokens
 
 
 @dataclass

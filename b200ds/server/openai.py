@@ -390,6 +390,24 @@ def _logprobs_param(body: dict, chat: bool) -> Optional[int]:
     return n
 
 
+def _penalty_params(body: dict) -> dict:
+    """presence_penalty / frequency_penalty (OpenAI, -2..2), repetition_penalty
+    (> 0), min_p (0..1), min_tokens (>= 0)."""
+    def num(name, default, lo, hi, cast=float):
+        v = body.get(name)
+        if v is None:
+            return default
+        v = cast(v)
+        if not lo <= v <= hi:
+            raise ValueError(f"{name} must be in [{lo}, {hi}]")
+        return v
+    return dict(presence_penalty=num("presence_penalty", 0.0, -2.0, 2.0),
+                frequency_penalty=num("frequency_penalty", 0.0, -2.0, 2.0),
+                repetition_penalty=num("repetition_penalty", 1.0, 1e-3, 100.0),
+                min_p=num("min_p", 0.0, 0.0, 1.0),
+                min_tokens=num("min_tokens", 0, 0, 1 << 30, int))
+
+
 def _lp_json(tok, lps, chat: bool, offset: int = 0) -> dict:
     """Engine log-probabilities -> the OpenAI response field (chat: `content`
     entries with token, logprob, bytes, top_logprobs; completions: parallel
@@ -421,6 +439,7 @@ def _params(body: dict, default_max: int = 16, chat: bool = False) -> SamplingPa
         ignore_eos=bool(body.get("ignore_eos", False)),
         stop_token_ids=list(stop_ids),
         logprobs=_logprobs_param(body, chat),
+        **_penalty_params(body),
     )
 
 

@@ -210,3 +210,13 @@ def test_engine_failure_while_streaming():
         err = json.loads(lines[-2][6:])
         assert "injected step failure" in err["error"]["message"]
     worker.stop()
+
+
+def test_penalty_parameters(client):
+    ok = client.post("/v1/completions", json={"prompt": [5, 6, 7, 5, 6, 7], "max_tokens": 6, "temperature": 0,
+                                              "presence_penalty": 1.5, "frequency_penalty": 0.5,
+                                              "repetition_penalty": 1.3, "min_p": 0.05, "min_tokens": 2})
+    assert ok.status_code == 200 and len(ok.json()["choices"][0]["token_ids"]) == 6
+    for bad in ({"presence_penalty": 3}, {"repetition_penalty": 0}, {"min_p": 1.5}, {"min_tokens": -1}):
+        r = client.post("/v1/completions", json=dict({"prompt": [1], "max_tokens": 1}, **bad))
+        assert r.status_code == 400, bad
