@@ -2,8 +2,11 @@
 
 Endpoints: POST /v1/completions, POST /v1/chat/completions (both with
 ``stream: true`` server-sent events, ``n``, ``stop`` strings and token ids,
-``seed``, and log-probabilities: ``logprobs`` / ``top_logprobs``), GET
-/v1/models, GET /health, GET /metrics (Prometheus text).
+``seed``, penalties, ``min_p`` / ``min_tokens``, ``max_completion_tokens``,
+``stream_options.include_usage`` and log-probabilities: ``logprobs`` /
+``top_logprobs``), POST /tokenize and /detokenize, GET /v1/models, GET
+/health (503 after an engine failure or while a step overruns the watchdog),
+GET /metrics (Prometheus text).
 
 One engine thread owns the Engine and runs `step()` whenever requests are
 pending; HTTP handlers enqueue requests and await their tokens through
@@ -431,7 +434,7 @@ def _lp_json(tok, lps, chat: bool, offset: int = 0) -> dict:
 def _params(body: dict, default_max: int = 16, chat: bool = False) -> SamplingParams:
     stop_ids = body.get("stop_token_ids") or []
     return SamplingParams(
-        max_tokens=int(body.get("max_tokens") or default_max),
+        max_tokens=int(body.get("max_completion_tokens") or body.get("max_tokens") or default_max),
         temperature=float(body.get("temperature", 1.0) if body.get("temperature") is not None else 1.0),
         top_p=float(body.get("top_p", 1.0) or 1.0),
         top_k=int(body.get("top_k", 0) or 0),
@@ -552,6 +555,19 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
                     if not done:              # client disconnected: free the request
                         worker.cancel(q)
 
+            usage = bool((body.get("stream_options") or {}).get("include_usage"))
+
+            def _final(n_out: int) -> str:
+                """Closing events: the usage chunk (stream_options.include_usage)
+                and [DONE]."""
+                tail = "data: [DONE]\n\n"
+                if not usage:
+                    return tail
+                u = {"prompt_tokens": len(ids), "completion_tokens": n_out, "total_tokens": len(ids) + n_out}
+                ev = {"id": rid, "object": obj + ".chunk", "created": created, "model": model_name,
+                      "choices": [], "usage": u}
+                return f"data: {json.dumps(ev)}\n\n" + tail
+
             async def _chunks():
                 ids_all: List[int] = []
                 sent = 0                      # characters of the decoded text already streamed
@@ -560,7 +576,7 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
                     kind, val = ev[0], ev[1]
                     if kind == "error":
                         yield f"data: {json.dumps({'error': {'message': f'engine error: {val}', 'type': 'server_error'}})}\n\n"
-                        yield "data: [DONE]\n\n"
+                        yield _final(len(ids_all))
                         return
                     if kind == "tokens":
                         lp_field = None
@@ -583,13 +599,13 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
                             choice = ({"index": 0, "delta": {}, "finish_reason": "stop"} if chat
                                       else {"index": 0, "text": "", "finish_reason": "stop"})
                             yield f"data: {json.dumps({'id': rid, 'object': obj + '.chunk', 'created': created, 'model': model_name, 'choices': [choice]})}\n\n"
-                            yield "data: [DONE]\n\n"
+                            yield _final(len(ids_all))
                             return
                     else:
                         choice = ({"index": 0, "delta": {}, "finish_reason": val} if chat
                                   else {"index": 0, "text": "", "finish_reason": val})
                         yield f"data: {json.dumps({'id': rid, 'object': obj + '.chunk', 'created': created, 'model': model_name, 'choices': [choice]})}\n\n"
-                        yield "data: [DONE]\n\n"
+                        yield _final(len(ids_all))
                         return
             return StreamingResponse(gen(), media_type="text/event-stream")
         out, text, reason, lps = await _collect(q, stops)
@@ -609,6 +625,21 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
     @app.get("/v1/models")
     async def models():
         return {"object": "list", "data": [{"id": model_name, "object": "model", "owned_by": "b200ds"}]}
+
+    @app.post("/tokenize")
+    async def tokenize(request: Request):
+        """{"prompt": text} or {"messages": [...]} -> token ids (chat template applied)."""
+        body = await request.json()
+        ids = _prompt_ids(body, chat="messages" in body)
+        return {"tokens": ids, "count": len(ids)}
+
+    @app.post("/detokenize")
+    async def detokenize(request: Request):
+        body = await request.json()
+        t = body.get("tokens")
+        if not isinstance(t, list) or not all(isinstance(i, int) for i in t):
+            raise HTTPException(400, "tokens must be a list of token ids")
+        return {"prompt": tok.decode(t)}
 
     @app.get("/health")
     async def health():

@@ -220,3 +220,19 @@ def test_penalty_parameters(client):
     for bad in ({"presence_penalty": 3}, {"repetition_penalty": 0}, {"min_p": 1.5}, {"min_tokens": -1}):
         r = client.post("/v1/completions", json=dict({"prompt": [1], "max_tokens": 1}, **bad))
         assert r.status_code == 400, bad
+
+
+def test_usage_chunk_max_completion_tokens_and_tokenize(client):
+    with client.stream("POST", "/v1/chat/completions", json={
+            "messages": [{"role": "user", "content": "hi"}], "max_completion_tokens": 3, "temperature": 0,
+            "stream": True, "stream_options": {"include_usage": True}}) as s:
+        lines = [l for l in s.iter_lines() if l.startswith("data: ")]
+    assert lines[-1] == "data: [DONE]"
+    last = json.loads(lines[-2][6:])
+    assert last["choices"] == [] and last["usage"]["completion_tokens"] == 3
+    t = client.post("/tokenize", json={"prompt": "hello"}).json()
+    assert t["count"] == len(t["tokens"]) > 0
+    assert client.post("/detokenize", json={"tokens": t["tokens"]}).json()["prompt"] == "hello"
+    chat = client.post("/tokenize", json={"messages": [{"role": "user", "content": "hello"}]}).json()
+    assert chat["count"] > t["count"]                     # the chat template adds its markers
+    assert client.post("/detokenize", json={"tokens": "x"}).status_code == 400
