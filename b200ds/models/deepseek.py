@@ -20,9 +20,8 @@ all-reduce + norm + quant), epa.py:1208 (o_proj GEMM + all-reduce).
 """
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass
-from typing import Dict, List, Optional
+from typing import List, Optional
 
 import torch
 

@@ -15,7 +15,6 @@ per-step work is that of the full model.
 """
 from __future__ import annotations
 
-import math
 from typing import List, Optional
 
 import torch

@@ -17,7 +17,6 @@ sqrtsoftplus.
 from __future__ import annotations
 
 import dataclasses
-import math
 from typing import Dict, List, Optional
 
 import torch

@@ -5,7 +5,6 @@ extension raises: there is no silent fallback.
 """
 from __future__ import annotations
 
-import math
 import os
 from typing import Optional
 

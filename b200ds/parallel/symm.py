@@ -12,7 +12,6 @@ Reference parity: symmetric-memory rendezvous of the EPA / LGP buffers
 """
 from __future__ import annotations
 
-from typing import Optional
 
 import torch
 import torch.distributed as dist

@@ -177,7 +177,6 @@ def test_abort_waiting_prefilling_running():
 
 def test_server_cancel_aborts_request():
     """A subscription whose client went away is aborted by the worker."""
-    import asyncio
     import time as _t
     from b200ds.engine.request import SamplingParams
     from b200ds.server.openai import EngineWorker

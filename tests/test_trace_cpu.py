@@ -1,6 +1,5 @@
 """Tracer host logic: phase spans from stamps, per-kind sums, disabled no-op,
 and the model's mark sequence (CPU, stamps supplied by the test)."""
-import torch
 
 
 def test_tracer_report_and_summary():

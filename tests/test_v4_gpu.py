@@ -84,8 +84,7 @@ def test_engram_hash_gather_gate():
     from b200ds import ops
     from b200ds.config import tiny_v4_config
     from b200ds.models.batch import build_batch
-    from b200ds.ops import EngramWeights, cuda, ref
-    from b200ds.models.deepseek import Linear
+    from b200ds.ops import cuda, ref
     cfg = tiny_v4_config(hidden_size=1024, engram_heads=8, engram_rows=4096)
     mults = torch.tensor([v - (1 << 64) if v >= (1 << 63) else v for v in ref.engram_multipliers(8)])
     toks = list(range(11, 90, 3))

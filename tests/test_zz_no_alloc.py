@@ -8,7 +8,6 @@ scratch arrays with the first call's contents still in them.
 This file sorts last so that a run stopping at the first failure has
 already run every other test."""
 import ctypes
-import glob
 import os
 
 import pytest
