@@ -671,6 +671,14 @@ def main(argv=None):
     ap.add_argument("--trace", action="store_true", help="device timestamps per layer phase")
     ap.add_argument("--mixed-steps", action="store_true", help="decode tokens ride along with prefill chunks")
     ap.add_argument("--extend-graphs", action="store_true", help="replay prefill chunks from CUDA graphs")
+    ap.add_argument("--page-size", type=int, default=64, help="tokens per KV page")
+    ap.add_argument("--max-prefill-tokens", type=int, default=16384, help="chunked-prefill budget per step")
+    ap.add_argument("--kv-cache-fraction", type=float, default=0.85, help="of free HBM after weights")
+    ap.add_argument("--graph-batch-sizes", default="1,2,4,8,16,32,64,128,256",
+                    help="decode CUDA-graph batch buckets (comma-separated)")
+    ap.add_argument("--no-prefill-tail", action="store_true", help="window-only late layers on every prefill row")
+    ap.add_argument("--comm", choices=("fused", "nccl"), default="fused",
+                    help="fused NVLink collectives or the NCCL baseline")
     ap.add_argument("--watchdog-timeout", type=float, default=300.0,
                     help="seconds one engine step may run before /health reports a stall (0: off)")
     ap.add_argument("--watchdog-exit", action="store_true", help="exit the process when the watchdog fires")
@@ -686,7 +694,10 @@ def main(argv=None):
                         cuda_graphs=not args.no_cuda_graphs, max_model_len=args.max_model_len,
                         enable_prefix_cache=not (args.no_prefix_cache or args.spec_mtp),
                         spec_ngram=args.spec_ngram, spec_mtp=args.spec_mtp, spec_k=args.spec_k, trace=args.trace,
-                        mixed_steps=args.mixed_steps, extend_graphs=args.extend_graphs)
+                        mixed_steps=args.mixed_steps, extend_graphs=args.extend_graphs, page_size=args.page_size,
+                        max_prefill_tokens=args.max_prefill_tokens, kv_cache_fraction=args.kv_cache_fraction,
+                        graph_batch_sizes=tuple(int(x) for x in args.graph_batch_sizes.split(",") if x),
+                        prefill_tail=not args.no_prefill_tail, comm_impl=args.comm)
     eng = load_engine(args.model, weights=args.weights, ecfg=ecfg)
     tok = load_tokenizer(args.model)
     eng.tokenizer = tok
