@@ -78,7 +78,8 @@ class Engine:
             self.mtp.allocate_kv(num_pages)
         self.radix = RadixCache(self.pool) if ecfg.enable_prefix_cache else None
         self.sched = Scheduler(self.pool, ecfg.max_num_seqs, ecfg.max_prefill_tokens, self.radix,
-                               mixed=ecfg.mixed_steps and not ecfg.dp_attention and not ecfg.spec_mtp)
+                               mixed=ecfg.mixed_steps and not ecfg.dp_attention and not ecfg.spec_mtp,
+                               policy=ecfg.schedule_policy)
         self.eos = eos_token_id
         self.tokenizer = tokenizer
         self._next_rid = 0

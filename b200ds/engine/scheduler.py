@@ -37,10 +37,19 @@ def prefill_target(r: Request) -> int:
     return len(r.prompt) if not r.output else r.total_len - 1
 
 
+LPM_MAX_QUEUE = 128
+
+
 class Scheduler:
     def __init__(self, pool: PagePool, max_num_seqs: int, max_prefill_tokens: int,
-                 radix: Optional[RadixCache] = None, mixed: bool = False):
+                 radix: Optional[RadixCache] = None, mixed: bool = False, policy: str = "fcfs"):
+        if policy not in ("fcfs", "lpm"):
+            raise ValueError(f"schedule policy {policy!r}: fcfs or lpm")
         self.pool = pool
+        # lpm: admit the waiting requests with the longest cached prefix first
+        # (more prefix-cache hits before those pages are evicted); arrival
+        # order breaks ties, and queues longer than LPM_MAX_QUEUE stay FCFS
+        self.policy = policy
         # mixed = True: a prefill step also carries one decode token of every
         # running request, so decoding does not stall behind long prompts
         self.mixed = mixed
@@ -109,6 +118,10 @@ class Scheduler:
             reqs, chunks, starts, sample = [], [], [], []
             cands = list(self.prefilling)
             self.prefilling = []
+            if self.policy == "lpm" and self.radix is not None and 1 < len(self.waiting) <= LPM_MAX_QUEUE:
+                order = sorted(self.waiting, key=lambda r: -self.radix.match_len(
+                    r.all_tokens[: prefill_target(r) - 1] if r.output else r.prompt[:-1]))
+                self.waiting = deque(order)
             while self.waiting and len(self.running) + len(cands) < self.max_num_seqs:
                 r = self.waiting.popleft()
                 self._admit(r)

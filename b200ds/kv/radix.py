@@ -58,6 +58,17 @@ class RadixCache:
         self.pool.retain(pages)
         return pages, nodes
 
+    def match_len(self, tokens: List[int]) -> int:
+        """Pages of the longest cached prefix, without retaining them or
+        touching their recency (for scheduling decisions)."""
+        node, n = self.root, 0
+        for ch in self._chunks(tokens):
+            node = node.children.get(ch)
+            if node is None:
+                break
+            n += 1
+        return n
+
     def unlock(self, nodes: List[_Node]) -> None:
         for n in nodes:
             n.locks -= 1

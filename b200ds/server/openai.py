@@ -677,6 +677,8 @@ def main(argv=None):
     ap.add_argument("--graph-batch-sizes", default="1,2,4,8,16,32,64,128,256",
                     help="decode CUDA-graph batch buckets (comma-separated)")
     ap.add_argument("--no-prefill-tail", action="store_true", help="window-only late layers on every prefill row")
+    ap.add_argument("--schedule-policy", choices=("fcfs", "lpm"), default="fcfs",
+                    help="admission order: arrival, or longest cached prefix first")
     ap.add_argument("--comm", choices=("fused", "nccl"), default="fused",
                     help="fused NVLink collectives or the NCCL baseline")
     ap.add_argument("--watchdog-timeout", type=float, default=300.0,
@@ -697,7 +699,8 @@ def main(argv=None):
                         mixed_steps=args.mixed_steps, extend_graphs=args.extend_graphs, page_size=args.page_size,
                         max_prefill_tokens=args.max_prefill_tokens, kv_cache_fraction=args.kv_cache_fraction,
                         graph_batch_sizes=tuple(int(x) for x in args.graph_batch_sizes.split(",") if x),
-                        prefill_tail=not args.no_prefill_tail, comm_impl=args.comm)
+                        prefill_tail=not args.no_prefill_tail, comm_impl=args.comm,
+                        schedule_policy=args.schedule_policy)
     eng = load_engine(args.model, weights=args.weights, ecfg=ecfg)
     tok = load_tokenizer(args.model)
     eng.tokenizer = tok

@@ -231,3 +231,38 @@ def test_logprobs_match_oracle_and_leave_tokens_unchanged():
     assert none.logprobs is None
     zero = eng.generate(prompts[:1], SamplingParams(max_tokens=3, logprobs=0))[0]
     assert all(top == [] for _, _, top in zero.logprobs) and len(zero.logprobs) == 3
+
+
+def test_lpm_policy_admits_the_longest_cached_prefix_first():
+    """schedule_policy lpm: with one free slot, a waiting request whose prompt
+    shares a cached prefix goes before an earlier one that shares nothing
+    (fcfs keeps arrival order); outputs are unchanged by the order."""
+    from b200ds.kv.radix import RadixCache
+    for policy, first in (("fcfs", "b"), ("lpm", "c")):
+        pool = PagePool(64, 4)
+        radix = RadixCache(pool)
+        shared = list(range(100, 116))                   # 4 full pages
+        pages = pool.alloc(4)
+        radix.insert(shared, pages)
+        pool.release(pages)
+        s = Scheduler(pool, max_num_seqs=1, max_prefill_tokens=64, radix=radix, policy=policy)
+        b = Request(1, list(range(1, 19)), SamplingParams())
+        c = Request(2, shared + [7, 8], SamplingParams())
+        s.add(b)
+        s.add(c)
+        st = s.next_step()
+        assert st.reqs == [b if first == "b" else c]
+        if first == "c":
+            assert c.cached == 16 and [len(x) for x in st.chunks] == [2]
+    import pytest
+    with pytest.raises(ValueError):
+        Scheduler(PagePool(8, 4), 1, 8, policy="random")
+    eng, cfg = _engine(True, schedule_policy="lpm")
+    ref_eng, _ = _engine(False)
+    g = torch.Generator().manual_seed(12)
+    shared = torch.randint(0, cfg.vocab_size, (24,), generator=g).tolist()
+    prompts = [shared + [1, 2], torch.randint(0, cfg.vocab_size, (9,), generator=g).tolist(), shared + [3]]
+    eng.generate(prompts[:1], SamplingParams(max_tokens=2))
+    got = [o.token_ids for o in eng.generate(prompts, SamplingParams(max_tokens=5))]
+    want = [o.token_ids for o in ref_eng.generate(prompts, SamplingParams(max_tokens=5))]
+    assert got == want
