@@ -47,6 +47,12 @@ class GenerateOutput:
     tpot_s: float
     text: Optional[str] = None
     logprobs: Optional[List[tuple]] = None   # per token: (token, logprob, [(alt, logprob), ...])
+    prompt_logprobs: Optional[List[Optional[tuple]]] = None   # per prompt token (None for the first)
+
+
+def _wants_plp(step) -> bool:
+    """A prefill step with a request that asked for prompt log-probabilities."""
+    return step.kind == "prefill" and any(r.params.prompt_logprobs is not None for r in step.reqs)
 
 
 def _wants_lp(reqs) -> bool:
@@ -145,7 +151,7 @@ class Engine:
             except GraphCaptureFailed as e:    # agreed on every rank: eager decode from now on
                 self._graphs_off("decode", e)
         if (step.kind == "prefill" and self.graphs is not None and self.ecfg.extend_graphs and self.mtp is None
-                and self.extend_graphs_ok):
+                and self.extend_graphs_ok and not _wants_plp(step)):
             if self.extend_graphs is None:
                 from .cuda_graph import ExtendGraphRunner
                 self.extend_graphs = ExtendGraphRunner(self, self.graphs.max_pages)
@@ -158,10 +164,7 @@ class Engine:
                 toks = self._sample(step, logits)
                 self._note_lp(step.reqs, logits, range(len(toks)), [[t] for t in toks], step.sample)
                 return toks
-        fb = build_batch(seqs, self.ecfg.page_size, device="cpu")
-        fb.tail_from = self._tail_from(step)
-        fb = self._to_device(fb)
-        logits = self.model.forward(fb)
+        logits = self._eager_logits(step, seqs)
         toks = self._sample(step, logits)
         self._note_lp(step.reqs, logits, range(len(toks)), [[t] for t in toks], step.sample)
         if self.mtp is not None and step.kind == "prefill":
@@ -194,16 +197,61 @@ class Engine:
                 self._graphs_off("decode", e)
         if step is None:      # idle rank: one dummy token on the scratch page
             seqs = [{"tokens": [0], "start": 0, "pages": [0]}]
-        fb = build_batch(seqs, self.ecfg.page_size, device="cpu")
-        fb.dp_tmax = max(max_tok, 1)
-        fb.tail_from = None if step is None else self._tail_from(step)
-        fb = self._to_device(fb)
-        logits = self.model.forward(fb)
         if step is None:
+            fb = self._to_device(build_batch(seqs, self.ecfg.page_size, device="cpu"))
+            fb.dp_tmax = max(max_tok, 1)
+            self.model.forward(fb)
             return []
+        logits = self._eager_logits(step, seqs, dp_tmax=max(max_tok, 1))
         toks = self._sample(step, logits)
         self._note_lp(step.reqs, logits, range(len(toks)), [[t] for t in toks], step.sample)
         return toks
+
+    def _eager_logits(self, step: Step, seqs: List[dict], dp_tmax: int = 0) -> torch.Tensor:
+        """Eager forward of a step; returns the logits of each sequence's last
+        row.  Prefill chunks of requests that asked for prompt log-probabilities
+        get logits at every row, recorded here."""
+        fb = build_batch(seqs, self.ecfg.page_size, device="cpu")
+        fb.dp_tmax = dp_tmax
+        fb.tail_from = self._tail_from(step)
+        sel = None
+        if _wants_plp(step):
+            idx, sel, off = [], [], 0
+            for r, ch in zip(step.reqs, step.chunks):
+                n = len(ch)
+                idx.extend(range(off, off + n) if r.params.prompt_logprobs is not None else [off + n - 1])
+                sel.append(len(idx) - 1)
+                off += n
+            fb.last_idx = torch.tensor(idx, dtype=torch.int64)
+        fb = self._to_device(fb)
+        logits = self.model.forward(fb)
+        if sel is None:
+            return logits
+        self._note_prompt_lp(step, logits)
+        return logits[torch.tensor(sel, device=logits.device)]
+
+    def _note_prompt_lp(self, step: Step, logits: torch.Tensor) -> None:
+        """Row j of a prompt-logprob request's chunk (position p = start + j)
+        scores prompt token p + 1; positions already recorded (a recompute
+        after preemption) are skipped."""
+        row = 0
+        for r, ch, st in zip(step.reqs, step.chunks, step.starts):
+            m = r.params.prompt_logprobs
+            if m is None:
+                row += 1
+                continue
+            if not r.prompt_lp:
+                r.prompt_lp.append(None)
+            lp = torch.log_softmax(logits[row: row + len(ch)].float(), -1)
+            tv, ti = lp.topk(m, -1) if m > 0 else (None, None)
+            for j in range(len(ch)):
+                p = st + j
+                if p + 1 >= len(r.prompt) or len(r.prompt_lp) != p + 1:
+                    continue
+                t = r.prompt[p + 1]
+                top = list(zip(ti[j].tolist(), tv[j].tolist())) if m > 0 else []
+                r.prompt_lp.append((t, float(lp[j, t]), top))
+            row += len(ch)
 
     def _tail_from(self, step: Step) -> Optional[torch.Tensor]:
         """Prefill tail of a step (window-only late layers, V4 family): per
@@ -214,7 +262,8 @@ class Engine:
         (both reuse rows a tail would leave out)."""
         c = self.model.cfg
         if (step.kind != "prefill" or not c.is_v4 or c.late_layer_start is None or c.late_window <= 0
-                or not self.ecfg.prefill_tail or self.radix is not None or self.mtp is not None):
+                or not self.ecfg.prefill_tail or self.radix is not None or self.mtp is not None
+                or _wants_plp(step)):
             return None
         from .scheduler import prefill_target
         n_pre = len(step.reqs) - step.decode_rows
@@ -319,6 +368,11 @@ class Engine:
             self.stats["decode_tokens"] += sum(len(m) for m in multi)
         for r, smp, new in zip(st.reqs, st.sample, multi):
             if not smp:
+                continue
+            if r.params.max_tokens <= 0:      # prompt only (e.g. prompt log-probabilities): no token
+                r.finished, r.finish_reason, r.t_done = True, "length", now
+                self.sched.finish(r)
+                done.append(r)
                 continue
             lps = self._step_lp.get(r.rid)
             for k, t in enumerate(new):
@@ -598,5 +652,6 @@ class Engine:
             text = self.tokenizer.decode(r.output) if self.tokenizer is not None else None
             outs.append(GenerateOutput(r.rid, len(r.prompt), list(r.output), r.finish_reason or "length",
                                        (r.t_first or r.t_arrive) - r.t_arrive, tpot, text,
-                                       list(r.logprobs) if r.params.logprobs is not None else None))
+                                       list(r.logprobs) if r.params.logprobs is not None else None,
+                                       list(r.prompt_lp) if r.params.prompt_logprobs is not None else None))
         return outs

@@ -23,6 +23,8 @@ class SamplingParams:
     repetition_penalty: float = 1.0  # prompt / output tokens: positive logits / r, negative * r
     min_p: float = 0.0              # drop tokens below min_p x the top probability (temperature > 0)
     min_tokens: int = 0             # no end-of-sequence / stop token before this many output tokens
+    prompt_logprobs: Optional[int] = None  # log-probability of every prompt token (+ top-n); computes the
+                                           # whole prompt (no prefix-cache reuse)
 
 
 @dataclass
@@ -43,6 +45,8 @@ class Request:
     token_times: List[float] = field(default_factory=list)
     # per output token (SamplingParams.logprobs set): (token, logprob, [(alt token, logprob), ...])
     logprobs: List[tuple] = field(default_factory=list)
+    # per prompt position (prompt_logprobs set): None for the first token, then (token, logprob, top-n)
+    prompt_lp: List[Optional[tuple]] = field(default_factory=list)
     gen: Optional[torch.Generator] = None
 
     @property

@@ -80,7 +80,7 @@ class Scheduler:
         return True
 
     def _admit(self, r: Request) -> None:
-        if self.radix is not None and not r.pages:
+        if self.radix is not None and not r.pages and r.params.prompt_logprobs is None:
             # leave at least one token to compute so the step yields logits
             pages, nodes = self.radix.match(r.all_tokens[: prefill_target(r) - 1] if r.output
                                             else r.prompt[:-1])

@@ -165,7 +165,8 @@ class EngineWorker:
                     self.subs[rid] = (loop, q, len(r.output), r)
                     alive = _post(loop, q, ("tokens", new_toks, lps))
                 if r.finished:
-                    _post(loop, q, ("done", r.finish_reason))
+                    _post(loop, q, ("done", r.finish_reason,
+                                    r.prompt_lp if r.params.prompt_logprobs is not None else None))
                     self.metrics.finish(r)
                     del self.subs[rid]
                 elif not alive:               # the handler's event loop is gone
@@ -227,7 +228,7 @@ class DPEngineWorker(EngineWorker):
             if eng.sched.has_work:
                 self.metrics.step_time.append(time.perf_counter() - t0)
             for upd in _dp_gather(ps, _dp_updates(self.own)):
-                for gid, toks, fin, reason, r, lps in upd:
+                for gid, toks, fin, reason, r, lps, plp in upd:
                     if gid not in self.subs:     # aborted meanwhile
                         continue
                     loop, q, sent, _ = self.subs[gid]
@@ -235,7 +236,7 @@ class DPEngineWorker(EngineWorker):
                     if not alive and not fin:
                         self.cancel(q)
                     if fin:
-                        _post(loop, q, ("done", reason))
+                        _post(loop, q, ("done", reason, plp))
                         if r is not None:
                             self.metrics.finish(r)
                         del self.subs[gid]
@@ -265,7 +266,8 @@ def _dp_updates(own) -> list:
         lps = list(r.logprobs[sent:]) if r.params.logprobs is not None else None
         st[1] = len(r.output)
         if toks or r.finished:
-            out.append((gid, list(toks), r.finished, r.finish_reason, None, lps))
+            plp = list(r.prompt_lp) if r.finished and r.params.prompt_logprobs is not None else None
+            out.append((gid, list(toks), r.finished, r.finish_reason, None, lps, plp))
         if r.finished:
             del own[gid]
     return out
@@ -393,6 +395,19 @@ def _logprobs_param(body: dict, chat: bool) -> Optional[int]:
     return n
 
 
+def _max_tokens(body: dict, default: int) -> int:
+    """max_completion_tokens or max_tokens (0 allowed: the prompt only, e.g.
+    with echo + logprobs to score it)."""
+    v = body.get("max_completion_tokens")
+    v = body.get("max_tokens") if v is None else v
+    if v is None:
+        return default
+    v = int(v)
+    if v < 0:
+        raise ValueError("max_tokens must be >= 0")
+    return v
+
+
 def _penalty_params(body: dict) -> dict:
     """presence_penalty / frequency_penalty (OpenAI, -2..2), repetition_penalty
     (> 0), min_p (0..1), min_tokens (>= 0)."""
@@ -411,7 +426,7 @@ def _penalty_params(body: dict) -> dict:
                 min_tokens=num("min_tokens", 0, 0, 1 << 30, int))
 
 
-def _lp_json(tok, lps, chat: bool, offset: int = 0) -> dict:
+def _lp_json(tok, lps, chat: bool, offset: int = 0, prompt=None) -> dict:
     """Engine log-probabilities -> the OpenAI response field (chat: `content`
     entries with token, logprob, bytes, top_logprobs; completions: parallel
     tokens / token_logprobs / top_logprobs / text_offset lists)."""
@@ -420,21 +435,26 @@ def _lp_json(tok, lps, chat: bool, offset: int = 0) -> dict:
             s = tok.decode([t])
             return {"token": s, "logprob": lp, "bytes": list(s.encode("utf-8")), "token_id": t}
         return {"content": [dict(ent(t, lp), top_logprobs=[ent(a, alp) for a, alp in top]) for t, lp, top in lps]}
-    toks, offs = [], []
-    for t, _, _ in lps:
+    toks, offs, vals, tops = [], [], [], []
+    ent = list(lps)
+    if prompt is not None:            # echo: the prompt's tokens first (the first one has no log-probability)
+        ids, plp = prompt
+        plp = plp or [None] * len(ids)
+        ent = [(t, None, None) if e is None else e for t, e in zip(ids, plp)] + ent
+    for t, lp, top in ent:
         s = tok.decode([t])
         toks.append(s)
         offs.append(offset)
         offset += len(s)
-    return {"tokens": toks, "token_logprobs": [lp for _, lp, _ in lps],
-            "top_logprobs": [{tok.decode([a]): alp for a, alp in top} for _, _, top in lps],
-            "text_offset": offs}
+        vals.append(lp)
+        tops.append(None if top is None else {tok.decode([a]): alp for a, alp in top})
+    return {"tokens": toks, "token_logprobs": vals, "top_logprobs": tops, "text_offset": offs}
 
 
 def _params(body: dict, default_max: int = 16, chat: bool = False) -> SamplingParams:
     stop_ids = body.get("stop_token_ids") or []
     return SamplingParams(
-        max_tokens=int(body.get("max_completion_tokens") or body.get("max_tokens") or default_max),
+        max_tokens=_max_tokens(body, default_max),
         temperature=float(body.get("temperature", 1.0) if body.get("temperature") is not None else 1.0),
         top_p=float(body.get("top_p", 1.0) or 1.0),
         top_k=int(body.get("top_k", 0) or 0),
@@ -442,6 +462,7 @@ def _params(body: dict, default_max: int = 16, chat: bool = False) -> SamplingPa
         ignore_eos=bool(body.get("ignore_eos", False)),
         stop_token_ids=list(stop_ids),
         logprobs=_logprobs_param(body, chat),
+        prompt_logprobs=(_logprobs_param(body, chat) if body.get("echo") and not chat else None),
         **_penalty_params(body),
     )
 
@@ -477,9 +498,11 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
 
     async def _collect(q, stops):
         """Tokens of one subscription until it finishes (or a stop string
-        appears): (token ids, text, finish reason)."""
+        appears): (token ids, text, finish reason, log-probabilities, prompt
+        log-probabilities)."""
         out: List[int] = []
         lps: List[tuple] = []
+        plp = None
         reason = "length"
         text = None
         try:
@@ -500,13 +523,14 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
                             break
                 else:
                     reason = val
+                    plp = ev[2] if len(ev) > 2 else None
                     break
         except HTTPException:
             raise
         except BaseException:              # cancelled (client gone)
             worker.cancel(q)
             raise
-        return out, (tok.decode(out) if text is None else text), reason, lps
+        return out, (tok.decode(out) if text is None else text), reason, lps, plp
 
     async def _handle(request: Request, chat: bool):
         if not worker.healthy():
@@ -526,11 +550,15 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
         stops = body.get("stop") or []
         stops = [stops] if isinstance(stops, str) else [x for x in stops if isinstance(x, str) and x]
 
-        def _choice(i, out, text, reason, lps):
+        echo = bool(body.get("echo")) and not chat
+
+        def _choice(i, out, text, reason, lps, plp=None):
+            if echo:
+                text = tok.decode(ids) + text
             c = ({"index": i, "message": {"role": "assistant", "content": text}, "finish_reason": reason} if chat
                  else {"index": i, "text": text, "token_ids": out, "finish_reason": reason})
             if params.logprobs is not None:
-                c["logprobs"] = _lp_json(tok, lps, chat)
+                c["logprobs"] = _lp_json(tok, lps, chat, prompt=(ids, plp) if echo else None)
             return c
         if n > 1:
             # n independent samples of the prompt (seed + i when a seed is given)
@@ -538,8 +566,8 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
             qs = [await _run(ids, dataclasses.replace(params, seed=None if params.seed is None else params.seed + i))
                   for i in range(n)]
             results = [await _collect(q, stops) for q in qs]
-            choices = [_choice(i, out, text, reason, lps) for i, (out, text, reason, lps) in enumerate(results)]
-            gen_tok = sum(len(o) for o, _, _, _ in results)
+            choices = [_choice(i, *res) for i, res in enumerate(results)]
+            gen_tok = sum(len(res[0]) for res in results)
             return JSONResponse({"id": rid, "object": obj, "created": created, "model": model_name,
                                  "choices": choices, "usage": {"prompt_tokens": len(ids), "completion_tokens": gen_tok,
                                                                "total_tokens": len(ids) + gen_tok}})
@@ -571,6 +599,10 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
             async def _chunks():
                 ids_all: List[int] = []
                 sent = 0                      # characters of the decoded text already streamed
+                if echo:                      # the prompt's text first
+                    ev0 = {"id": rid, "object": obj + ".chunk", "created": created, "model": model_name,
+                           "choices": [{"index": 0, "text": tok.decode(ids), "token_ids": [], "finish_reason": None}]}
+                    yield f"data: {json.dumps(ev0)}\n\n"
                 while True:
                     ev = await q.get()
                     kind, val = ev[0], ev[1]
@@ -608,8 +640,9 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
                         yield _final(len(ids_all))
                         return
             return StreamingResponse(gen(), media_type="text/event-stream")
-        out, text, reason, lps = await _collect(q, stops)
-        choice = _choice(0, out, text, reason, lps)
+        res = await _collect(q, stops)
+        out = res[0]
+        choice = _choice(0, *res)
         return JSONResponse({"id": rid, "object": obj, "created": created, "model": model_name, "choices": [choice],
                              "usage": {"prompt_tokens": len(ids), "completion_tokens": len(out),
                                        "total_tokens": len(ids) + len(out)}})

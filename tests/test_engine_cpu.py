@@ -266,3 +266,30 @@ def test_lpm_policy_admits_the_longest_cached_prefix_first():
     got = [o.token_ids for o in eng.generate(prompts, SamplingParams(max_tokens=5))]
     want = [o.token_ids for o in ref_eng.generate(prompts, SamplingParams(max_tokens=5))]
     assert got == want
+
+
+def test_prompt_logprobs_under_chunked_prefill_match_oracle():
+    """prompt_logprobs: every prompt token after the first gets the model's
+    log-probability (and top-n) from the row before it, across prefill
+    chunks and with the prefix cache on (such requests recompute the whole
+    prompt); max_tokens=0 returns after the prompt without a token."""
+    from b200ds.config import EngineConfig
+    from b200ds.models.reference import ReferenceModel, init_weights
+    eng, cfg = _engine(True, max_prefill_tokens=7)
+    g = torch.Generator().manual_seed(21)
+    prompt = torch.randint(0, cfg.vocab_size, (19,), generator=g).tolist()
+    eng.generate([prompt], SamplingParams(max_tokens=2))               # the prompt's pages are now cached
+    out = eng.generate([prompt, prompt[:9]], [SamplingParams(max_tokens=3, prompt_logprobs=2),
+                                              SamplingParams(max_tokens=0, prompt_logprobs=0)])
+    oracle = ReferenceModel(cfg, init_weights(cfg, 0))
+    for o, p in zip(out, (prompt, prompt[:9])):
+        oracle.reset(1)
+        want = torch.log_softmax(oracle.forward(torch.tensor([p]), 0)[0].float(), -1)
+        assert len(o.prompt_logprobs) == len(p) and o.prompt_logprobs[0] is None
+        for j in range(1, len(p)):
+            t, lp, top = o.prompt_logprobs[j]
+            assert t == p[j] and abs(lp - float(want[j - 1, t])) < 1e-3
+            assert [a for a, _ in top] == want[j - 1].topk(len(top)).indices.tolist() if top else True
+    assert len(out[0].token_ids) == 3 and out[1].token_ids == [] and out[1].finish_reason == "length"
+    plain = eng.generate([prompt], SamplingParams(max_tokens=3))[0]
+    assert plain.token_ids == out[0].token_ids and plain.prompt_logprobs is None

@@ -236,3 +236,25 @@ def test_usage_chunk_max_completion_tokens_and_tokenize(client):
     chat = client.post("/tokenize", json={"messages": [{"role": "user", "content": "hello"}]}).json()
     assert chat["count"] > t["count"]                     # the chat template adds its markers
     assert client.post("/detokenize", json={"tokens": "x"}).status_code == 400
+
+
+def test_echo_prompt_logprobs_and_zero_max_tokens(client):
+    """Completions with echo + logprobs score the prompt (the lm-eval-harness
+    loglikelihood request): the prompt's tokens come first in the logprobs,
+    the first with no value; max_tokens 0 returns the prompt only."""
+    r = client.post("/v1/completions", json={"prompt": [5, 6, 7, 8, 9], "max_tokens": 0, "echo": True,
+                                             "logprobs": 1, "temperature": 0}).json()
+    c = r["choices"][0]
+    lp = c["logprobs"]
+    assert c["token_ids"] == [] and len(lp["tokens"]) == 5 and lp["token_logprobs"][0] is None
+    assert all(v is not None and v <= 0 for v in lp["token_logprobs"][1:]) and lp["top_logprobs"][0] is None
+    assert r["usage"]["completion_tokens"] == 0
+    both = client.post("/v1/completions", json={"prompt": [5, 6, 7, 8, 9], "max_tokens": 2, "echo": True,
+                                                "logprobs": 0, "temperature": 0}).json()["choices"][0]
+    assert len(both["logprobs"]["tokens"]) == 7
+    assert both["logprobs"]["token_logprobs"][1:5] == pytest.approx(lp["token_logprobs"][1:5], abs=1e-5)
+    with client.stream("POST", "/v1/completions", json={"prompt": "ab", "max_tokens": 2, "echo": True,
+                                                        "temperature": 0, "stream": True}) as s:
+        events = [json.loads(l[6:]) for l in s.iter_lines() if l.startswith("data: ") and l != "data: [DONE]"]
+    assert events[0]["choices"][0]["text"] == "ab"
+    assert client.post("/v1/completions", json={"prompt": [1], "max_tokens": -1}).status_code == 400
