@@ -196,11 +196,9 @@ class Engine:
             except GraphCaptureFailed as e:    # agreed on every rank: eager decode from now on
                 self._graphs_off("decode", e)
         if step is None:      # idle rank: one dummy token on the scratch page
-            seqs = [{"tokens": [0], "start": 0, "pages": [0]}]
-        if step is None:
-            fb = self._to_device(build_batch(seqs, self.ecfg.page_size, device="cpu"))
+            fb = build_batch([{"tokens": [0], "start": 0, "pages": [0]}], self.ecfg.page_size, device="cpu")
             fb.dp_tmax = max(max_tok, 1)
-            self.model.forward(fb)
+            self.model.forward(self._to_device(fb))
             return []
         logits = self._eager_logits(step, seqs, dp_tmax=max(max_tok, 1))
         toks = self._sample(step, logits)
