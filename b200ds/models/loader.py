@@ -10,6 +10,7 @@ from __future__ import annotations
 import glob
 import json
 import os
+from collections.abc import Mapping
 from typing import Dict, Iterable, List, Optional
 
 import torch
@@ -29,7 +30,7 @@ def _quantize(w: torch.Tensor, fmt: str, device) -> object:
     if fmt == "mxfp8":
         rows = w.shape[0]
         if w.shape[0] % 128:
-            w = torch.cat([w, torch.zeros(128 - w.shape[0] % 128, w.shape[1], dtype=w.dtype)], 0)
+            w = torch.cat([w, torch.zeros(128 - w.shape[0] % 128, w.shape[1], dtype=w.dtype, device=w.device)], 0)
         wd = w.to(device)
         if wd.is_cuda:
             from .. import ops
@@ -117,6 +118,9 @@ def build_model(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState,
     def get(name) -> torch.Tensor:
         t = sd[name]
         si = sd.get(name + "_scale_inv")
+        if dev.type == "cuda":       # fp8 bytes cross the host link; dequantize on the device
+            t = t.to(dev)
+            si = si.to(dev) if si is not None else None
         if si is not None:
             N, K = t.shape
             s = si.float().repeat_interleave(128, 0)[:N].repeat_interleave(128, 1)[:, :K]
@@ -185,19 +189,48 @@ def build_model(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState,
 # safetensors checkpoints
 # ---------------------------------------------------------------------------
 
-def load_checkpoint(path: str, names: Optional[Iterable[str]] = None) -> Dict[str, torch.Tensor]:
-    """Read every tensor (or the listed ones) of a HF safetensors checkpoint
-    directory; fp8 tensors keep their `_scale_inv` companions."""
-    from safetensors import safe_open
-    out: Dict[str, torch.Tensor] = {}
-    want = set(names) if names is not None else None
-    files = sorted(glob.glob(os.path.join(path, "*.safetensors")))
-    for f in files:
+class LazyCheckpoint(Mapping):
+    """Read-on-access view of a HF safetensors checkpoint directory: the
+    constructor reads only the file headers (tensor name -> file); a tensor
+    is read from its (memory-mapped) file when the model builder asks for
+    it.  So a rank reads the weights it keeps - its expert slice, the
+    replicated / TP-split dense weights - and never the whole checkpoint
+    (the 671B fp8 checkpoint is ~690 GB; eight ranks each holding it in host
+    memory would not fit).  fp8 tensors keep their `_scale_inv` companions."""
+
+    def __init__(self, path: str, names: Optional[Iterable[str]] = None):
+        from safetensors import safe_open
+        want = set(names) if names is not None else None
+        self.path = path
+        self._where: Dict[str, str] = {}
+        for f in sorted(glob.glob(os.path.join(path, "*.safetensors"))):
+            with safe_open(f, framework="pt") as fh:
+                for k in fh.keys():
+                    if want is None or k in want or k.replace("_scale_inv", "") in want:
+                        self._where[k] = f
+        self.reads = 0
+
+    def __getitem__(self, k: str) -> torch.Tensor:
+        from safetensors import safe_open
+        f = self._where[k]
+        self.reads += 1
         with safe_open(f, framework="pt") as fh:
-            for k in fh.keys():
-                if want is None or k in want or k.replace("_scale_inv", "") in want:
-                    out[k] = fh.get_tensor(k)
-    return out
+            return fh.get_tensor(k)
+
+    def __iter__(self):
+        return iter(self._where)
+
+    def __len__(self) -> int:
+        return len(self._where)
+
+    def __contains__(self, k) -> bool:
+        return k in self._where
+
+
+def load_checkpoint(path: str, names: Optional[Iterable[str]] = None) -> LazyCheckpoint:
+    """The tensors (or the listed ones) of a HF safetensors checkpoint
+    directory, read when accessed (LazyCheckpoint)."""
+    return LazyCheckpoint(path, names)
 
 
 def save_checkpoint_fp8(sd: Dict[str, torch.Tensor], path: str, cfg: ModelConfig, shard_bytes: int = 1 << 30):

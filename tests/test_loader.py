@@ -71,3 +71,31 @@ def test_mtp_layer_from_checkpoint(tmp_path):
         assert eng.model.mtp is not None
         outs[mtp] = [o.token_ids for o in eng.generate(prompts, SamplingParams(max_tokens=6))]
     assert outs[True] == outs[False]
+
+
+def test_lazy_checkpoint_reads_only_this_ranks_weights(tmp_path):
+    """The checkpoint is read on access: an EP rank building its model reads
+    its own experts' tensors and none of the other ranks' experts."""
+    from b200ds.config import EngineConfig, tiny_config
+    from b200ds.models.loader import LazyCheckpoint, build_model, save_checkpoint_fp8
+    from b200ds.models.reference import init_weights
+    from b200ds.parallel.state import ParallelState
+    cfg = tiny_config()
+    save_checkpoint_fp8(init_weights(cfg, 0), str(tmp_path), cfg)
+    ck = LazyCheckpoint(str(tmp_path))
+    assert ck.reads == 0 and len(ck) > 0
+    seen = []
+    orig = LazyCheckpoint.__getitem__
+
+    def spy(self, k):
+        seen.append(k)
+        return orig(self, k)
+    LazyCheckpoint.__getitem__ = spy
+    try:
+        ps = ParallelState(world_size=2, rank=1, tp_size=2, ep_size=2, tp_rank=1, ep_rank=1)
+        build_model(cfg, EngineConfig(page_size=8, cuda_graphs=False, tp_size=2, ep_size=2), ps, ck, device="cpu")
+    finally:
+        LazyCheckpoint.__getitem__ = orig
+    experts = {int(k.split(".experts.")[1].split(".")[0]) for k in seen if ".experts." in k}
+    per = cfg.n_routed_experts // 2
+    assert experts == set(range(per, 2 * per))
