@@ -29,6 +29,9 @@ class ByteTokenizer:
             parts.append("<|assistant|>")
         return "".join(parts)
 
+    def encode_chat(self, messages) -> List[int]:
+        return self.encode(self.apply_chat_template(messages))
+
 
 class HFTokenizer:
     def __init__(self, path: str):
@@ -44,6 +47,12 @@ class HFTokenizer:
 
     def apply_chat_template(self, messages, add_generation_prompt: bool = True) -> str:
         return self.tok.apply_chat_template(messages, tokenize=False, add_generation_prompt=add_generation_prompt)
+
+    def encode_chat(self, messages) -> List[int]:
+        """Token ids of the chat template: the template writes its own BOS,
+        so the text is not encoded again with special tokens added."""
+        text = self.apply_chat_template(messages)
+        return self.tok.encode(text, add_special_tokens=False)
 
 
 def load_tokenizer(path: Optional[str]):

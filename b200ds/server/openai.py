@@ -485,8 +485,7 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
             msgs = body.get("messages")
             if not isinstance(msgs, list):
                 raise HTTPException(400, "messages must be a list")
-            text = tok.apply_chat_template(msgs)
-            return tok.encode(text)
+            return tok.encode_chat(msgs)
         p = body.get("prompt")
         if isinstance(p, list) and all(isinstance(i, int) for i in p):
             return p
