@@ -99,3 +99,32 @@ def test_lazy_checkpoint_reads_only_this_ranks_weights(tmp_path):
     experts = {int(k.split(".experts.")[1].split(".")[0]) for k in seen if ".experts." in k}
     per = cfg.n_routed_experts // 2
     assert experts == set(range(per, 2 * per))
+
+
+def test_deepseek_v3_hf_config_json():
+    """The published DeepSeek-V3 config.json fields map onto the 671B preset
+    (fp8 checkpoint -> MXFP8 serving formats; unknown keys ignored)."""
+    from b200ds.config import ModelConfig, PRESETS
+    d = {"architectures": ["DeepseekV3ForCausalLM"], "model_type": "deepseek_v3", "vocab_size": 129280,
+         "hidden_size": 7168, "intermediate_size": 18432, "moe_intermediate_size": 2048, "num_hidden_layers": 61,
+         "num_nextn_predict_layers": 1, "num_attention_heads": 128, "num_key_value_heads": 128,
+         "n_shared_experts": 1, "n_routed_experts": 256, "ep_size": 1, "routed_scaling_factor": 2.5,
+         "kv_lora_rank": 512, "q_lora_rank": 1536, "qk_rope_head_dim": 64, "v_head_dim": 128,
+         "qk_nope_head_dim": 128, "topk_method": "noaux_tc", "n_group": 8, "topk_group": 4,
+         "num_experts_per_tok": 8, "moe_layer_freq": 1, "first_k_dense_replace": 3, "norm_topk_prob": True,
+         "scoring_func": "sigmoid", "hidden_act": "silu", "max_position_embeddings": 163840, "rms_norm_eps": 1e-6,
+         "rope_theta": 10000, "rope_scaling": {"beta_fast": 32, "beta_slow": 1, "factor": 40, "mscale": 1.0,
+                                               "mscale_all_dim": 1.0, "original_max_position_embeddings": 4096,
+                                               "type": "yarn"},
+         "tie_word_embeddings": False, "torch_dtype": "bfloat16", "bos_token_id": 0, "eos_token_id": 1,
+         "quantization_config": {"activation_scheme": "dynamic", "fmt": "e4m3", "quant_method": "fp8",
+                                 "weight_block_size": [128, 128]}}
+    c = ModelConfig.from_hf(d)
+    p = PRESETS["deepseek-v3-671b"]()
+    for f in ("vocab_size", "hidden_size", "num_hidden_layers", "num_attention_heads", "q_lora_rank", "kv_lora_rank",
+              "qk_nope_head_dim", "qk_rope_head_dim", "v_head_dim", "n_routed_experts", "num_experts_per_tok",
+              "n_group", "topk_group", "first_k_dense_replace", "moe_intermediate_size", "intermediate_size"):
+        assert getattr(c, f) == getattr(p, f), f
+    assert c.dense_format == c.expert_format == "mxfp8" and c.num_nextn_predict_layers == 1
+    assert abs(c.softmax_scale - p.softmax_scale) < 1e-9 and c.rope_scaling["factor"] == 40
+    assert 600e9 < c.num_params() < 700e9
