@@ -71,4 +71,26 @@ def load_engine(model: Union[str, ModelConfig] = "tiny", weights: Union[str, dic
         raise ValueError(f"unknown model {model!r}")
     ecfg = ecfg or EngineConfig()
     m = build_model_from(cfg, ecfg, weights, device=device, seed=seed)
-    return Engine(m, ecfg)
+    eos, tok = None, None
+    if isinstance(model, str) and os.path.isdir(model):
+        eos = _eos_id(model)
+        from .engine.tokenizer import load_tokenizer
+        tok = load_tokenizer(model)
+        if eos is None:
+            eos = getattr(tok, "eos_token_id", None)
+    return Engine(m, ecfg, eos_token_id=eos, tokenizer=tok)
+
+
+def _eos_id(path: str):
+    """End-of-sequence id of a checkpoint directory: generation_config.json,
+    else config.json (the first id when a list is given)."""
+    import json
+    import os
+    for f in ("generation_config.json", "config.json"):
+        p = os.path.join(path, f)
+        if os.path.exists(p):
+            with open(p) as fh:
+                v = json.load(fh).get("eos_token_id")
+            if v is not None:
+                return int(v[0] if isinstance(v, list) else v)
+    return None

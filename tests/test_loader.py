@@ -128,3 +128,16 @@ def test_deepseek_v3_hf_config_json():
     assert c.dense_format == c.expert_format == "mxfp8" and c.num_nextn_predict_layers == 1
     assert abs(c.softmax_scale - p.softmax_scale) < 1e-9 and c.rope_scaling["factor"] == 40
     assert 600e9 < c.num_params() < 700e9
+
+
+def test_checkpoint_dir_sets_eos(tmp_path):
+    import json
+    from b200ds import EngineConfig, load_engine
+    from b200ds.config import tiny_config
+    from b200ds.models.loader import save_checkpoint_fp8
+    from b200ds.models.reference import init_weights
+    cfg = tiny_config()
+    save_checkpoint_fp8(init_weights(cfg, 0), str(tmp_path), cfg)
+    (tmp_path / "generation_config.json").write_text(json.dumps({"eos_token_id": [7, 9]}))
+    eng = load_engine(str(tmp_path), ecfg=EngineConfig(page_size=8, cuda_graphs=False), device="cpu")
+    assert eng.eos == 7
