@@ -618,6 +618,14 @@ class Engine:
         self._mtp_chain(st.reqs, draft, hid, [n + len(o) + 1 for o, n in zip(out, st.starts)])
         return out
 
+    def gauges(self) -> Dict[str, float]:
+        """Current queue and KV-pool state and the scheduler's counters."""
+        sc = self.sched
+        return {"running": len(sc.running), "prefilling": len(sc.prefilling), "waiting": len(sc.waiting),
+                "kv_pages_total": self.pool.num_pages, "kv_pages_free": self.pool.num_free,
+                "admitted_prompt_tokens": sc.admitted_prompt_tokens, "prefix_hit_tokens": sc.prefix_hit_tokens,
+                "preemptions": sc.preemptions}
+
     def _check_device_errors(self) -> None:
         """Every device-side wait in the fused collectives is bounded; a wait
         that ran out (a peer that stopped pushing) leaves an error word on

@@ -57,6 +57,10 @@ class Scheduler:
         self.max_num_seqs = max_num_seqs
         self.max_prefill_tokens = max_prefill_tokens
         self.waiting: Deque[Request] = deque()
+        # counters for the metrics endpoint
+        self.admitted_prompt_tokens = 0         # tokens to cache at admission (prompts, recomputes)
+        self.prefix_hit_tokens = 0              # of those, found in the prefix cache
+        self.preemptions = 0
         self.prefilling: List[Request] = []      # admitted, prompt not fully cached
         self.running: List[Request] = []
 
@@ -88,6 +92,8 @@ class Scheduler:
             r.prefix_nodes = nodes
             r.prefix_pages = len(pages)
             r.cached = len(pages) * self.pool.page_size
+        self.admitted_prompt_tokens += prefill_target(r)
+        self.prefix_hit_tokens += r.cached
 
     def release(self, r: Request, cache_prefix: bool = True) -> None:
         if self.radix is not None and cache_prefix:
@@ -103,6 +109,7 @@ class Scheduler:
         if not self.running:
             return False
         v = self.running.pop()
+        self.preemptions += 1
         self.release(v)
         v.cached = 0
         self.waiting.appendleft(v)

@@ -336,7 +336,7 @@ class _Metrics:
         if r.t_done is not None and len(r.output) > 1:
             self.tpot.append((r.t_done - r.t_first) / (len(r.output) - 1))
 
-    def prometheus(self, engine_stats=None, switches=None) -> str:
+    def prometheus(self, engine_stats=None, switches=None, gauges=None) -> str:
         def q(xs, p):
             if not xs:
                 return 0.0
@@ -357,6 +357,15 @@ class _Metrics:
         for k in ("steps", "prefill_tokens", "decode_tokens", "spec_proposed", "spec_accepted"):
             if k in st:
                 lines.append(f"b200ds_engine_{k}_total {int(st[k])}")
+        g = gauges or {}
+        for k in ("running", "prefilling", "waiting", "kv_pages_total", "kv_pages_free"):
+            if k in g:
+                lines.append(f"b200ds_{k} {int(g[k])}")
+        for k in ("admitted_prompt_tokens", "prefix_hit_tokens", "preemptions"):
+            if k in g:
+                lines.append(f"b200ds_{k}_total {int(g[k])}")
+        if g.get("admitted_prompt_tokens"):
+            lines.append(f"b200ds_prefix_cache_hit_ratio {g['prefix_hit_tokens'] / g['admitted_prompt_tokens']:.6f}")
         for k, v in sorted((switches or {}).items()):
             lines.append(f'b200ds_switch{{name="{k}"}} {int(bool(v))}')
         return "\n".join(lines) + "\n"
@@ -681,7 +690,8 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
     @app.get("/metrics")
     async def metrics():
         from ..utils import levers
-        return PlainTextResponse(worker.metrics.prometheus(worker.engine.stats, levers.switches()))
+        return PlainTextResponse(worker.metrics.prometheus(worker.engine.stats, levers.switches(),
+                                                           worker.engine.gauges()))
 
     return app
 

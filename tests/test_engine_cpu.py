@@ -293,3 +293,15 @@ def test_prompt_logprobs_under_chunked_prefill_match_oracle():
     assert len(out[0].token_ids) == 3 and out[1].token_ids == [] and out[1].finish_reason == "length"
     plain = eng.generate([prompt], SamplingParams(max_tokens=3))[0]
     assert plain.token_ids == out[0].token_ids and plain.prompt_logprobs is None
+
+
+def test_gauges_count_prefix_hits():
+    eng, cfg = _engine(True)
+    p = list(range(40, 72))                                  # 32 tokens = 4 pages of 8
+    eng.generate([p], SamplingParams(max_tokens=2))
+    g0 = eng.gauges()
+    assert g0["admitted_prompt_tokens"] == 32 and g0["prefix_hit_tokens"] == 0
+    eng.generate([p + [5]], SamplingParams(max_tokens=2))
+    g1 = eng.gauges()
+    assert g1["admitted_prompt_tokens"] == 65 and g1["prefix_hit_tokens"] == 32
+    assert g1["running"] == 0 and g1["waiting"] == 0 and g1["kv_pages_free"] <= g1["kv_pages_total"]
