@@ -175,35 +175,46 @@ class Engine:
         """One lockstep DP-attention forward.  All ranks run the same kind of
         forward: the decode graph of the largest rank's bucket when every
         rank decodes, else eager with dp_tmax = the largest rank's tokens.
-        Returns None when no rank has work, [] for an idle rank that joined
-        with a dummy forward, else this rank's sampled tokens."""
+        Speculative drafts (n-gram) join the agreement: when any rank
+        verifies, every rank runs eagerly and the verifying ranks score their
+        drafts in the same forward.  Returns None when no rank has work, else
+        (tokens, accepted lists): ([], None) for an idle rank that joined with
+        a dummy forward, (tokens, None) after a plain step, (None, accepted
+        tokens per request) after a verify."""
         import torch.distributed as dist
-        ntok = 0 if step is None else sum(len(c) for c in step.chunks)
+        drafts = self._propose_drafts(step)
+        ntok = 0 if step is None else sum(len(c) for c in step.chunks) + sum(len(d) for d in drafts or [])
         nseq = 0 if step is None else len(step.reqs)
         prefill = step is not None and step.kind == "prefill"
         lp = step is not None and _wants_lp(step.reqs)
-        v = torch.tensor([int(prefill), ntok, nseq, int(step is not None), int(lp)], dtype=torch.int64)
+        v = torch.tensor([int(prefill), ntok, nseq, int(step is not None), int(lp), int(drafts is not None)],
+                         dtype=torch.int64)
         dist.all_reduce(v, op=dist.ReduceOp.MAX, group=self.ps.cpu_group)
-        any_prefill, max_tok, max_seq, any_work, any_lp = (int(x) for x in v)
+        any_prefill, max_tok, max_seq, any_work, any_lp, any_verify = (int(x) for x in v)
         if not any_work:
             return None
         seqs = [] if step is None else [{"tokens": ch, "start": st, "pages": r.pages}
                                         for r, ch, st in zip(step.reqs, step.chunks, step.starts)]
-        if not any_prefill and not any_lp and self.graphs is not None and self.graphs.can_run(max_seq):
+        if (not any_prefill and not any_lp and not any_verify and self.graphs is not None
+                and self.graphs.can_run(max_seq)):
             try:
                 toks = self.graphs.run(step, seqs, bucket=self.graphs._bucket(max_seq))
-                return [] if toks is None else toks
+                return [] if toks is None else toks, None
             except GraphCaptureFailed as e:    # agreed on every rank: eager decode from now on
                 self._graphs_off("decode", e)
         if step is None:      # idle rank: one dummy token on the scratch page
             fb = build_batch([{"tokens": [0], "start": 0, "pages": [0]}], self.ecfg.page_size, device="cpu")
             fb.dp_tmax = max(max_tok, 1)
             self.model.forward(self._to_device(fb))
-            return []
+            return [], None
+        if drafts is not None:  # this rank verifies its drafts in the same lockstep forward
+            seqs = [{"tokens": ch + d, "start": s, "pages": r.pages}
+                    for r, ch, s, d in zip(step.reqs, step.chunks, step.starts, drafts)]
+            return None, self._verify_eager(step, seqs, drafts, dp_tmax=max(max_tok, 1))
         logits = self._eager_logits(step, seqs, dp_tmax=max(max_tok, 1))
         toks = self._sample(step, logits)
         self._note_lp(step.reqs, logits, range(len(toks)), [[t] for t in toks], step.sample)
-        return toks
+        return toks, None
 
     def _eager_logits(self, step: Step, seqs: List[dict], dp_tmax: int = 0) -> torch.Tensor:
         """Eager forward of a step; returns the logits of each sequence's last
@@ -336,9 +347,10 @@ class Engine:
         multi = None
         self._step_lp: Dict[int, list] = {}
         if self.dp:
-            toks = self._dp_forward(st)
+            res = self._dp_forward(st)
             if st is None:
                 return []
+            toks, multi = res
         elif st is None:
             return []
         else:
@@ -413,19 +425,13 @@ class Engine:
         (logits at every position).  Returns the accepted tokens per request
         (accepted draft prefix + the model's next token), or None when no
         request has a draft (plain decode then)."""
-        if self.dp or not st.reqs or any(needs_adjust(r.params) for r in st.reqs):
-            return None       # drafts are verified against raw logits; adjusted requests decode one token
+        if self.dp:
+            return None       # DP ranks verify inside the lockstep forward (_dp_forward)
+        drafts = self._propose_drafts(st)
+        if drafts is None:
+            return None
         sampling = any(r.params.temperature > 0 for r in st.reqs)
         want_lp = _wants_lp(st.reqs)
-        drafts = []
-        for r in st.reqs:
-            room = r.params.max_tokens - len(r.output) - 1
-            d = self._ngram_draft(r)[: max(0, room)]
-            if d and not self.sched._ensure_pages(r, r.cached + 1 + len(d)):
-                d = []
-            drafts.append(d)
-        if not any(drafts):
-            return None
         seqs = [{"tokens": ch + d, "start": s, "pages": r.pages}
                 for r, ch, s, d in zip(st.reqs, st.chunks, st.starts, drafts)]
         k = self.ecfg.spec_k
@@ -442,17 +448,40 @@ class Engine:
                 else:
                     starts = [i * (1 + k) for i in range(len(seqs))]
                     return self._accept(st, drafts, pred, starts)
+        return self._verify_eager(st, seqs, drafts)
+
+    def _propose_drafts(self, st: Step) -> Optional[List[List[int]]]:
+        """n-gram drafts of a decode step's requests (pages reserved for them),
+        or None when no request has one or a request needs adjusted logits
+        (drafts are verified against the raw logits)."""
+        if (st is None or st.kind != "decode" or self.ecfg.spec_ngram <= 0 or self.mtp is not None or not st.reqs
+                or any(needs_adjust(r.params) for r in st.reqs)):
+            return None
+        drafts = []
+        for r in st.reqs:
+            room = r.params.max_tokens - len(r.output) - 1
+            d = self._ngram_draft(r)[: max(0, room)]
+            if d and not self.sched._ensure_pages(r, r.cached + 1 + len(d)):
+                d = []
+            drafts.append(d)
+        return drafts if any(drafts) else None
+
+    def _verify_eager(self, st: Step, seqs: List[dict], drafts, dp_tmax: int = 0) -> List[List[int]]:
+        """One forward over [newest token + draft] per request with logits at
+        every row, then greedy or speculative-sampling acceptance."""
         fb = build_batch(seqs, self.ecfg.page_size, device="cpu")
         fb.last_idx = torch.arange(fb.num_tokens, dtype=torch.int64)     # logits at every position
+        fb.dp_tmax = dp_tmax
         fb = self._to_device(fb)
         logits = self.model.forward(fb)
-        pred = logits.argmax(-1).tolist()
         starts, off = [], 0
         for d in drafts:
             starts.append(off)
             off += 1 + len(d)
-        out = (self._accept_sampled(st, drafts, logits, starts) if sampling
-               else self._accept(st, drafts, pred, starts))
+        if any(r.params.temperature > 0 for r in st.reqs):
+            out = self._accept_sampled(st, drafts, logits, starts)
+        else:
+            out = self._accept(st, drafts, logits.argmax(-1).tolist(), starts)
         self._note_lp(st.reqs, logits, starts, out)
         return out
 

@@ -58,3 +58,41 @@ def test_dp2_ep2_matches_single():
         _, logs = _run(cfg, EngineConfig(page_size=8, cuda_graphs=False), [_prompts(cfg)[i] for i in mine],
                        [1] * len(mine))
         assert (first_logits - logs[0][1]).abs().max() < 1e-4
+
+
+def _spec_rank(rank, world):
+    from b200ds import build_model_from
+    from b200ds.config import EngineConfig, tiny_config
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.reference import init_weights
+    from b200ds.parallel.state import init_parallel
+    ps = init_parallel(backend="gloo", dp_attention=True)
+    cfg = tiny_config()
+    ecfg = EngineConfig(page_size=8, cuda_graphs=False, tp_size=1, ep_size=world, dp_attention=True,
+                        spec_ngram=3, spec_k=3)
+    eng = Engine(build_model_from(cfg, ecfg, init_weights(cfg, 0), device="cpu", ps=ps), ecfg)
+    mine = [i for i in range(3) if i % world == rank]
+    prompts = _spec_prompts(cfg)
+    outs = eng.generate([prompts[i] for i in mine], [SamplingParams(max_tokens=(16, 9, 20)[i]) for i in mine])
+    return mine, [o.token_ids for o in outs], eng.stats.get("spec_proposed", 0), eng.stats["steps"]
+
+
+def _spec_prompts(cfg):
+    g = torch.Generator().manual_seed(5)
+    base = torch.randint(0, cfg.vocab_size, (5,), generator=g).tolist()
+    return [base * 4, torch.randint(0, cfg.vocab_size, (11,), generator=g).tolist(), base[:3] * 5]
+
+
+def test_dp2_speculative_ngram_matches_single():
+    """n-gram speculative decoding under DP attention: ranks that verify
+    drafts and ranks that decode plainly share one lockstep forward per
+    step; every request's tokens equal a single-process run without
+    speculation."""
+    from b200ds.config import EngineConfig, tiny_config
+    cfg = tiny_config()
+    ref, _ = _run(cfg, EngineConfig(page_size=8, cuda_graphs=False), _spec_prompts(cfg), [16, 9, 20])
+    res = run_ranks(_spec_rank, 2)
+    assert sum(r[2] for r in res) > 0                    # drafts were proposed and verified
+    for mine, toks, _, _ in res:
+        assert toks == [ref[i] for i in mine]
