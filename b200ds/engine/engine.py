@@ -676,17 +676,37 @@ class Engine:
         reqs = [self.add_request(p, sp) for p, sp in zip(prompts, params)]
         while any(not r.finished for r in reqs):
             self.step()
+        self._drain_dp()
+        return [self._output(r) for r in reqs]
+
+    def stream(self, prompts: Sequence[Union[str, Sequence[int]]],
+               params: Union[SamplingParams, Sequence[SamplingParams], None] = None):
+        """Like generate, but yields (prompt index, new token ids) after every
+        step that produced tokens for that prompt, then ("done", outputs)."""
+        if params is None or isinstance(params, SamplingParams):
+            params = [params or SamplingParams()] * len(prompts)
+        reqs = [self.add_request(p, sp) for p, sp in zip(prompts, params)]
+        sent = [0] * len(reqs)
+        while any(not r.finished for r in reqs):
+            self.step()
+            for i, r in enumerate(reqs):
+                if len(r.output) > sent[i]:
+                    yield i, list(r.output[sent[i]:])
+                    sent[i] = len(r.output)
+        self._drain_dp()
+        yield "done", [self._output(r) for r in reqs]
+
+    def _drain_dp(self) -> None:
         if self.dp:
             # keep stepping (as an idle rank) until every rank is done
             while self._dp_forward(None) is not None:
                 pass
-        outs = []
-        for r in reqs:
-            n = len(r.output)
-            tpot = (r.t_done - r.t_first) / (n - 1) if n > 1 else 0.0
-            text = self.tokenizer.decode(r.output) if self.tokenizer is not None else None
-            outs.append(GenerateOutput(r.rid, len(r.prompt), list(r.output), r.finish_reason or "length",
-                                       (r.t_first or r.t_arrive) - r.t_arrive, tpot, text,
-                                       list(r.logprobs) if r.params.logprobs is not None else None,
-                                       list(r.prompt_lp) if r.params.prompt_logprobs is not None else None))
-        return outs
+
+    def _output(self, r: Request) -> GenerateOutput:
+        n = len(r.output)
+        tpot = (r.t_done - r.t_first) / (n - 1) if n > 1 else 0.0
+        text = self.tokenizer.decode(r.output) if self.tokenizer is not None else None
+        return GenerateOutput(r.rid, len(r.prompt), list(r.output), r.finish_reason or "length",
+                              (r.t_first or r.t_arrive) - r.t_arrive, tpot, text,
+                              list(r.logprobs) if r.params.logprobs is not None else None,
+                              list(r.prompt_lp) if r.params.prompt_logprobs is not None else None)

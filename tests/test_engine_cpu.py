@@ -305,3 +305,17 @@ def test_gauges_count_prefix_hits():
     g1 = eng.gauges()
     assert g1["admitted_prompt_tokens"] == 65 and g1["prefix_hit_tokens"] == 32
     assert g1["running"] == 0 and g1["waiting"] == 0 and g1["kv_pages_free"] <= g1["kv_pages_total"]
+
+
+def test_stream_yields_tokens_as_they_come():
+    eng, cfg = _engine(False)
+    prompts = [list(range(3, 12)), list(range(30, 35))]
+    want = [o.token_ids for o in eng.generate(prompts, SamplingParams(max_tokens=5))]
+    got, final = [[], []], None
+    for i, toks in eng.stream(prompts, SamplingParams(max_tokens=5)):
+        if i == "done":
+            final = toks
+        else:
+            assert toks
+            got[i].extend(toks)
+    assert got == want and [o.token_ids for o in final] == want
