@@ -606,10 +606,12 @@ class Engine:
         self._mtp_chain(reqs, [draft[k] for k in idx], hid[idx], n_next)
 
     def _mtp_decode(self, st: Step) -> Optional[List[List[int]]]:
-        """Verify the MTP drafts (greedy) in one main-model forward with logits
-        and hidden states at every row, then run the MTP module over the
-        accepted tokens for the next drafts."""
-        if any(r.params.temperature > 0 or needs_adjust(r.params) for r in st.reqs):
+        """Verify the MTP drafts in one main-model forward with logits and
+        hidden states at every row (greedy acceptance, or speculative sampling
+        for temperature > 0: the drafts are the module's argmax, a
+        deterministic function of the context), then run the MTP module over
+        the accepted tokens for the next drafts."""
+        if any(needs_adjust(r.params) for r in st.reqs):
             for r in st.reqs:
                 r.mtp_drafts = []
             return None
@@ -626,13 +628,15 @@ class Engine:
         fb.last_idx = torch.arange(fb.num_tokens, dtype=torch.int64)     # logits at every position
         fb = self._to_device(fb)
         logits = self.model.forward(fb)
-        pred = logits.argmax(-1).tolist()
         H = self.model.last_residual
         starts, off = [], 0
         for d in drafts:
             starts.append(off)
             off += 1 + len(d)
-        out = self._accept(st, drafts, pred, starts)
+        if any(r.params.temperature > 0 for r in st.reqs):
+            out = self._accept_sampled(st, drafts, logits, starts)
+        else:
+            out = self._accept(st, drafts, logits.argmax(-1).tolist(), starts)
         self._note_lp(st.reqs, logits, starts, out)
         rows, prev = [], []
         for r, o, s0, n in zip(st.reqs, out, starts, st.starts):

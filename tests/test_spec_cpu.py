@@ -200,3 +200,30 @@ def test_logprobs_under_speculative_decoding():
     assert spec.token_ids == plain.token_ids and len(spec.logprobs) == len(plain.logprobs)
     for a, b in zip(spec.logprobs, plain.logprobs):
         assert a[0] == b[0] and abs(a[1] - b[1]) < 1e-3 and [t for t, _ in a[2]] == [t for t, _ in b[2]]
+
+
+def test_mtp_speculative_sampling():
+    """MTP drafts with temperature > 0 go through speculative sampling: with
+    top_k 1 the sampling distribution is the argmax, so the tokens equal
+    greedy decoding; with a wider distribution drafts are still proposed
+    and accepted and the outputs are reproducible per seed."""
+    from b200ds import build_model_from
+    from b200ds.config import EngineConfig, tiny_config
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.reference import init_weights
+    cfg = tiny_config(num_nextn_predict_layers=1)
+    sd = init_weights(cfg, 0)
+    g = torch.Generator().manual_seed(3)
+    prompts = torch.randint(0, cfg.vocab_size, (2, 13), generator=g).tolist()
+
+    def run(sp, **kw):
+        ecfg = EngineConfig(page_size=8, cuda_graphs=False, enable_prefix_cache=False, **kw)
+        eng = Engine(build_model_from(cfg, ecfg, sd, device="cpu"), ecfg)
+        return [o.token_ids for o in eng.generate(prompts, sp)], eng.stats
+    greedy, _ = run(SamplingParams(max_tokens=10))
+    top1, st = run(SamplingParams(max_tokens=10, temperature=0.8, top_k=1, seed=1), spec_mtp=True, spec_k=3)
+    assert top1 == greedy and st.get("spec_proposed", 0) > 0
+    a, st = run(SamplingParams(max_tokens=10, temperature=1.0, seed=7), spec_mtp=True, spec_k=3)
+    b, _ = run(SamplingParams(max_tokens=10, temperature=1.0, seed=7), spec_mtp=True, spec_k=3)
+    assert a == b and st.get("spec_proposed", 0) > 0 and all(len(t) == 10 for t in a)
