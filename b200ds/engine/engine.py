@@ -126,10 +126,34 @@ class Engine:
         if isinstance(prompt, str):
             assert self.tokenizer is not None, "text prompts need a tokenizer"
             prompt = self.tokenizer.encode(prompt)
-        r = Request(self._next_rid, list(prompt), params or SamplingParams())
+        params = params or SamplingParams()
+        self.check_request(prompt, params)
+        r = Request(self._next_rid, list(prompt), params)
         self._next_rid += 1
         self.sched.add(r)
         return r
+
+    def check_request(self, prompt_ids: Sequence[int], params: SamplingParams) -> None:
+        """Raise ValueError for a request the engine cannot serve (checked
+        before it is queued, so one bad request never reaches a step): empty
+        prompt, ids outside the vocabulary, prompt + max_tokens beyond
+        max_model_len or beyond the whole KV pool."""
+        n = len(prompt_ids)
+        if n == 0:
+            raise ValueError("the prompt is empty")
+        V = self.cfg.vocab_size
+        bad = next((t for t in prompt_ids if not (isinstance(t, int) and 0 <= t < V)), None)
+        if bad is not None:
+            raise ValueError(f"token id {bad!r} is outside the vocabulary [0, {V})")
+        if params.max_tokens < 0:
+            raise ValueError("max_tokens must be >= 0")
+        total = n + params.max_tokens
+        if total > self.ecfg.max_model_len:
+            raise ValueError(f"the maximum context length is {self.ecfg.max_model_len} tokens; the request needs "
+                             f"{total} ({n} in the prompt, {params.max_tokens} to generate)")
+        if self.pool.pages_for(total) > self.pool.num_pages - 1:       # page 0 is the scratch page
+            raise ValueError(f"the request needs {total} tokens of KV cache; the pool holds "
+                             f"{(self.pool.num_pages - 1) * self.pool.page_size}")
 
     def abort(self, r: Request) -> None:
         """Stop a request now (client gone): it leaves the schedule, its pages

@@ -138,9 +138,14 @@ class EngineWorker:
     def _loop(self):
         eng = self.engine
         while not self._stop.is_set():
-            new = self._admit()
-            for prompt, params, loop, q in new:
-                r = eng.add_request(prompt, params)
+            new = []
+            for prompt, params, loop, q in self._admit():
+                try:
+                    r = eng.add_request(prompt, params)
+                except ValueError as e:        # refused before it is queued (and never broadcast)
+                    _post(loop, q, ("error", str(e)))
+                    continue
+                new.append((prompt, params, loop, q))
                 self.subs[r.rid] = (loop, q, 0, r)
                 self.metrics.requests += 1
             aborts = self._cancelled()
@@ -211,6 +216,11 @@ class DPEngineWorker(EngineWorker):
             new = self._admit()
             batch = []
             for prompt, params, loop, q in new:
+                try:
+                    eng.check_request(prompt, params)
+                except ValueError as e:        # refused before it is assigned to a rank
+                    _post(loop, q, ("error", str(e)))
+                    continue
                 gid = self.next_gid
                 self.next_gid += 1
                 self.subs[gid] = (loop, q, 0, None)
@@ -235,6 +245,10 @@ class DPEngineWorker(EngineWorker):
                     alive = _post(loop, q, ("tokens", toks, lps)) if toks else True
                     if not alive and not fin:
                         self.cancel(q)
+                    if fin and reason and reason.startswith("error: "):
+                        _post(loop, q, ("error", reason[len("error: "):]))
+                        del self.subs[gid]
+                        continue
                     if fin:
                         _post(loop, q, ("done", reason, plp))
                         if r is not None:
@@ -252,10 +266,22 @@ def _dp_abort(eng, gids, own) -> None:
             eng.abort(st[0])
 
 
+class _Refused:
+    """A request its owner rank could not queue (reported back as an error)."""
+
+    def __init__(self, params, msg: str):
+        self.params, self.output, self.logprobs, self.prompt_lp = params, [], [], []
+        self.finished, self.finish_reason = True, "error: " + msg
+
+
 def _dp_admit(eng, ps, batch, own) -> None:
     for prompt, spd, owner, gid in batch:
         if owner == ps.rank:
-            own[gid] = [eng.add_request(prompt, SamplingParams(**spd)), 0]
+            sp = SamplingParams(**spd)
+            try:
+                own[gid] = [eng.add_request(prompt, sp), 0]
+            except ValueError as e:
+                own[gid] = [_Refused(sp, str(e)), 0]
 
 
 def _dp_updates(own) -> list:
@@ -547,6 +573,7 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
         ids = _prompt_ids(body, chat)
         try:
             params = _params(body, chat=chat)
+            worker.engine.check_request(ids, params)
         except ValueError as e:
             raise HTTPException(400, str(e))
         rid = f"{'chatcmpl' if chat else 'cmpl'}-{uuid.uuid4().hex[:16]}"

@@ -193,7 +193,7 @@ def test_server_cancel_aborts_request():
             self.items.append(item)
     w = EngineWorker(eng, None).start()
     lp = Loop()
-    w.submit(list(range(40)), SamplingParams(max_tokens=10000), lp, lp)
+    w.submit(list(range(40)), SamplingParams(max_tokens=8000), lp, lp)
     t0 = _t.time()
     while not any(ev[0] == "tokens" for ev in lp.items) and _t.time() - t0 < 60:
         _t.sleep(0.01)
@@ -319,3 +319,13 @@ def test_stream_yields_tokens_as_they_come():
             assert toks
             got[i].extend(toks)
     assert got == want and [o.token_ids for o in final] == want
+
+
+def test_check_request_limits():
+    import pytest
+    eng, cfg = _engine(False, max_model_len=64)
+    for prompt, mt in (([], 1), ([cfg.vocab_size], 1), ([-1], 1), (list(range(60)), 10), ([1, 2], -1)):
+        with pytest.raises(ValueError):
+            eng.add_request(prompt, SamplingParams(max_tokens=mt))
+    assert not eng.sched.has_work
+    eng.check_request(list(range(60)), SamplingParams(max_tokens=4))

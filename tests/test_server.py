@@ -259,3 +259,43 @@ def test_echo_prompt_logprobs_and_zero_max_tokens(client):
         events = [json.loads(l[6:]) for l in s.iter_lines() if l.startswith("data: ") and l != "data: [DONE]"]
     assert events[0]["choices"][0]["text"] == "ab"
     assert client.post("/v1/completions", json={"prompt": [1], "max_tokens": -1}).status_code == 400
+
+
+def test_invalid_requests_are_refused_alone(client):
+    """Requests the engine cannot serve get a 400 (empty prompt, ids outside
+    the vocabulary, context beyond max_model_len) and the server keeps
+    serving; submitted past the HTTP checks, the worker refuses just that
+    one."""
+    for body in ({"prompt": [], "max_tokens": 2}, {"prompt": [5, 99999], "max_tokens": 2},
+                 {"prompt": [5, 6], "max_tokens": 10 ** 6}):
+        r = client.post("/v1/completions", json=body)
+        assert r.status_code == 400, (body, r.text)
+    assert client.get("/health").status_code == 200
+    ok = client.post("/v1/completions", json={"prompt": [5, 6], "max_tokens": 3, "temperature": 0})
+    assert ok.status_code == 200 and len(ok.json()["choices"][0]["token_ids"]) == 3
+
+
+def test_worker_refuses_a_bad_request_without_failing():
+    import time
+    from b200ds.engine.request import SamplingParams
+    eng, worker, _ = _fresh_client()
+
+    class Loop:
+        def __init__(self):
+            self.items = []
+
+        def call_soon_threadsafe(self, fn, item):
+            fn(item)
+
+        def put_nowait(self, item):
+            self.items.append(item)
+    worker.start()
+    bad, good = Loop(), Loop()
+    worker.submit([], SamplingParams(max_tokens=2), bad, bad)
+    worker.submit([4, 5, 6], SamplingParams(max_tokens=2), good, good)
+    t0 = time.time()
+    while not any(ev[0] == "done" for ev in good.items) and time.time() - t0 < 30:
+        time.sleep(0.01)
+    worker.stop()
+    assert bad.items and bad.items[0][0] == "error" and "empty" in bad.items[0][1]
+    assert worker.healthy() and any(ev[0] == "done" for ev in good.items)
