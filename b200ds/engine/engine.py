@@ -127,8 +127,9 @@ class Engine:
             assert self.tokenizer is not None, "text prompts need a tokenizer"
             prompt = self.tokenizer.encode(prompt)
         params = params or SamplingParams()
+        prompt = [int(t) for t in prompt]      # python ints (tensor / numpy rows accepted)
         self.check_request(prompt, params)
-        r = Request(self._next_rid, list(prompt), params)
+        r = Request(self._next_rid, prompt, params)
         self._next_rid += 1
         self.sched.add(r)
         return r

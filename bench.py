@@ -208,7 +208,8 @@ def main():
     prompts = torch.randint(0, cfg.vocab_size, (args.batch, args.input_len), generator=g).tolist()
     if args.dp:
         prompts = prompts[ps.rank::world]
-    sp = SamplingParams(max_tokens=1 << 30, ignore_eos=True)
+    # every request decodes through the warm-up and both timed loops without finishing
+    sp = SamplingParams(max_tokens=ctx - args.input_len, ignore_eos=True)
     reqs = [eng.add_request(p, sp) for p in prompts]
 
     def barrier():

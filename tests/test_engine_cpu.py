@@ -329,3 +329,11 @@ def test_check_request_limits():
             eng.add_request(prompt, SamplingParams(max_tokens=mt))
     assert not eng.sched.has_work
     eng.check_request(list(range(60)), SamplingParams(max_tokens=4))
+
+
+def test_tensor_prompts_are_accepted():
+    eng, cfg = _engine(False)
+    p = torch.arange(3, 12)
+    a = eng.generate([p], SamplingParams(max_tokens=3))[0].token_ids
+    b = eng.generate([p.tolist()], SamplingParams(max_tokens=3))[0].token_ids
+    assert a == b
