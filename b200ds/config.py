@@ -330,6 +330,7 @@ class EngineConfig:
     extend_graphs: bool = False      # also replay prefill chunks up to 2048 tokens from per-bucket graphs
     graph_batch_sizes: tuple = (1, 2, 4, 8, 16, 32, 64, 128, 256)
     enable_prefix_cache: bool = True
+    host_kv_pages: int = 0           # >0: pages of pinned host memory behind the prefix cache (evicted pages move there)
     comm_impl: str = "fused"         # "fused" (own NVLink kernels) or "nccl" (baseline)
     gemm_impl: str = "native"        # "native" (own tcgen05 kernels) or "torch" (baseline)
     seed: int = 0

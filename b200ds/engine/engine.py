@@ -82,7 +82,11 @@ class Engine:
                 # the MTP row of a prefix's last position depends on the token after it
                 raise ValueError("spec_mtp runs without the prefix cache")
             self.mtp.allocate_kv(num_pages)
-        self.radix = RadixCache(self.pool) if ecfg.enable_prefix_cache else None
+        host = None
+        if ecfg.enable_prefix_cache and ecfg.host_kv_pages > 0:
+            from ..kv.host_cache import HostKVPool
+            host = HostKVPool(model.kv_tensors(), ecfg.host_kv_pages, ecfg.page_size)
+        self.radix = RadixCache(self.pool, host) if ecfg.enable_prefix_cache else None
         self.sched = Scheduler(self.pool, ecfg.max_num_seqs, ecfg.max_prefill_tokens, self.radix,
                                mixed=ecfg.mixed_steps and not ecfg.dp_attention and not ecfg.spec_mtp,
                                policy=ecfg.schedule_policy)
@@ -682,7 +686,9 @@ class Engine:
         return {"running": len(sc.running), "prefilling": len(sc.prefilling), "waiting": len(sc.waiting),
                 "kv_pages_total": self.pool.num_pages, "kv_pages_free": self.pool.num_free,
                 "admitted_prompt_tokens": sc.admitted_prompt_tokens, "prefix_hit_tokens": sc.prefix_hit_tokens,
-                "preemptions": sc.preemptions}
+                "preemptions": sc.preemptions,
+                "host_offloads": self.radix.offloads if self.radix is not None else 0,
+                "host_restores": self.radix.restores if self.radix is not None else 0}
 
     def _check_device_errors(self) -> None:
         """Every device-side wait in the fused collectives is bounded; a wait

@@ -157,6 +157,13 @@ class DeepseekModel:
             self.ix_scale = [torch.ones(slots, dtype=torch.float32, device=self.device)
                              for _ in self.layers]
 
+    def kv_tensors(self) -> List[torch.Tensor]:
+        """Every per-slot cache tensor ([slots, ...], slot = page * page_size +
+        offset): what one KV page holds across the model."""
+        out = list(self.kv_cache)
+        out += list(getattr(self, "ix_cache", []) or []) + list(getattr(self, "ix_scale", []) or [])
+        return out
+
     def kv_bytes_per_token(self) -> int:
         c = self.cfg
         per = c.kv_cache_dim * torch.tensor([], dtype=self.kv_dtype).element_size()

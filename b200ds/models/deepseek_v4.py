@@ -115,6 +115,15 @@ class DeepseekV4Model:
         if c.engram_layers:
             self.tok_cache = torch.full((slots,), -1, dtype=torch.int32, device=self.device)
 
+    def kv_tensors(self) -> List[torch.Tensor]:
+        """Every per-slot cache tensor ([slots, ...], slot = page * page_size +
+        offset): what one KV page holds across the model."""
+        out = list(self.kv_cache)
+        out += list(getattr(self, "ix_cache", []) or []) + list(getattr(self, "ix_scale", []) or [])
+        if self.tok_cache is not None:
+            out.append(self.tok_cache)
+        return out
+
     def kv_bytes_per_token(self) -> int:
         c = self.cfg
         es = torch.tensor([], dtype=self.kv_dtype).element_size()

@@ -387,7 +387,7 @@ class _Metrics:
         for k in ("running", "prefilling", "waiting", "kv_pages_total", "kv_pages_free"):
             if k in g:
                 lines.append(f"b200ds_{k} {int(g[k])}")
-        for k in ("admitted_prompt_tokens", "prefix_hit_tokens", "preemptions"):
+        for k in ("admitted_prompt_tokens", "prefix_hit_tokens", "preemptions", "host_offloads", "host_restores"):
             if k in g:
                 lines.append(f"b200ds_{k}_total {int(g[k])}")
         if g.get("admitted_prompt_tokens"):
@@ -746,6 +746,8 @@ def main(argv=None):
     ap.add_argument("--graph-batch-sizes", default="1,2,4,8,16,32,64,128,256",
                     help="decode CUDA-graph batch buckets (comma-separated)")
     ap.add_argument("--no-prefill-tail", action="store_true", help="window-only late layers on every prefill row")
+    ap.add_argument("--host-kv-pages", type=int, default=0,
+                    help="pinned host pages behind the prefix cache (evicted pages move there)")
     ap.add_argument("--schedule-policy", choices=("fcfs", "lpm"), default="fcfs",
                     help="admission order: arrival, or longest cached prefix first")
     ap.add_argument("--comm", choices=("fused", "nccl"), default="fused",
@@ -769,7 +771,7 @@ def main(argv=None):
                         max_prefill_tokens=args.max_prefill_tokens, kv_cache_fraction=args.kv_cache_fraction,
                         graph_batch_sizes=tuple(int(x) for x in args.graph_batch_sizes.split(",") if x),
                         prefill_tail=not args.no_prefill_tail, comm_impl=args.comm,
-                        schedule_policy=args.schedule_policy)
+                        schedule_policy=args.schedule_policy, host_kv_pages=args.host_kv_pages)
     eng = load_engine(args.model, weights=args.weights, ecfg=ecfg)
     tok = load_tokenizer(args.model)
     eng.tokenizer = tok
