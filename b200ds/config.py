@@ -236,6 +236,18 @@ def v3_nvfp4_config(**over) -> ModelConfig:
     return dataclasses.replace(ModelConfig(expert_format="nvfp4", dense_format="mxfp8"), **over)
 
 
+def kimi_k2_config(**over) -> ModelConfig:
+    """The DeepSeek-V3 architecture at Kimi-K2 widths (1.04T parameters): 64
+    heads, 384 routed experts top-8 in one group, one dense first layer,
+    vocab 163840 - the same engine path with more experts per rank."""
+    c = ModelConfig(vocab_size=163840, num_attention_heads=64, n_routed_experts=384, n_group=1, topk_group=1,
+                    first_k_dense_replace=1, routed_scaling_factor=2.827, rope_theta=50000.0,
+                    rope_scaling={"type": "yarn", "factor": 32.0, "original_max_position_embeddings": 4096,
+                                  "beta_fast": 1.0, "beta_slow": 1.0, "mscale": 1.0, "mscale_all_dim": 1.0},
+                    max_position_embeddings=131072)
+    return dataclasses.replace(c, **over)
+
+
 def small_gpu_config(**over) -> ModelConfig:
     """A V3-shaped model small enough for single-GPU unit tests (4 layers)."""
     c = ModelConfig(
@@ -304,6 +316,8 @@ PRESETS = {
     "deepseek-v3-671b": v3_671b_config,
     "deepseek-v3.2-sparse-671b": v32_sparse_config,
     "deepseek-v3-671b-nvfp4": v3_nvfp4_config,
+    "deepseek-r1-671b": v3_671b_config,
+    "kimi-k2-1t": kimi_k2_config,
     "small": small_gpu_config,
     "tiny-v4": tiny_v4_config,
     "small-v4": small_v4_gpu_config,

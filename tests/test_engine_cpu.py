@@ -337,3 +337,24 @@ def test_tensor_prompts_are_accepted():
     a = eng.generate([p], SamplingParams(max_tokens=3))[0].token_ids
     b = eng.generate([p.tolist()], SamplingParams(max_tokens=3))[0].token_ids
     assert a == b
+
+
+def test_single_group_many_experts_matches_oracle():
+    """The Kimi-K2 routing shape (one expert group, top-8 of many experts,
+    one dense first layer) on a tiny model: engine tokens equal the oracle's."""
+    from b200ds import build_model_from
+    from b200ds.config import EngineConfig, PRESETS, tiny_config
+    from b200ds.engine.engine import Engine
+    from b200ds.models.reference import ReferenceModel, init_weights
+    k2 = PRESETS["kimi-k2-1t"]()
+    assert k2.n_group == 1 and k2.n_routed_experts == 384 and 1.0e12 < k2.num_params() < 1.1e12
+    cfg = tiny_config(n_routed_experts=24, num_experts_per_tok=8, n_group=1, topk_group=1,
+                      routed_scaling_factor=2.827)
+    sd = init_weights(cfg, 0)
+    ecfg = EngineConfig(page_size=8, cuda_graphs=False)
+    eng = Engine(build_model_from(cfg, ecfg, sd, device="cpu"), ecfg)
+    g = torch.Generator().manual_seed(17)
+    prompts = torch.randint(0, cfg.vocab_size, (2, 12), generator=g)
+    outs = eng.generate(prompts.tolist(), SamplingParams(max_tokens=5))
+    toks, _ = ReferenceModel(cfg, sd).greedy(prompts, 5)
+    assert [o.token_ids for o in outs] == toks.tolist()
