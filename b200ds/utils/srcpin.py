@@ -4,7 +4,8 @@ The build records a digest of every native source under csrc/ next to the
 built library (`b200ds/_C.srcpin`).  Importing the CUDA op layer from a source
 tree whose csrc/ no longer matches that digest raises, so a library built
 from older sources is never run in place of the current kernels (switch
-`srcpin`, B200_SRCPIN=0 to skip the check).
+`srcpin`, B200_SRCPIN=0 to skip the check; a library without a pin file is
+announced, not refused).
 
 Reference parity: the reference pins the stock sources its levers patch by
 hash and turns a lever off when they drift (levers.py:172-194, *_PINS).
@@ -49,12 +50,16 @@ def write_pin(csrc: Optional[str] = None, pin_file: str = PIN_FILE) -> Optional[
 
 def check_pin(csrc: Optional[str] = None, pin_file: str = PIN_FILE) -> Optional[str]:
     """None when the built library matches the sources (or there is nothing
-    to compare), else a one-line reason."""
+    to compare: no csrc/, or a library built without a pin, which is only
+    announced), else a one-line reason."""
     cur = source_digest(csrc)
     if cur is None:
         return None
     if not os.path.exists(pin_file):
-        return "the native library has no source pin (built by an older setup.py): rebuild"
+        from . import levers
+        levers.announce("srcpin-missing", "native library without a source pin (not built by setup.py): "
+                        "its sources are not checked")
+        return None
     with open(pin_file) as f:
         pinned = f.read().strip()
     if pinned != cur:

@@ -12,7 +12,7 @@ def test_pin_detects_changed_sources(tmp_path):
     (csrc / "b.h").write_text("#pragma once\n")
     (csrc / "notes.txt").write_text("not a source")
     pin = str(tmp_path / "_C.srcpin")
-    assert check_pin(str(csrc), pin) is not None          # never built: no pin
+    assert check_pin(str(csrc), pin) is None              # no pin file: announced, not refused
     d0 = write_pin(str(csrc), pin)
     assert check_pin(str(csrc), pin) is None
     (csrc / "notes.txt").write_text("still not a source")
