@@ -335,7 +335,7 @@ class EngineConfig:
     max_model_len: int = 16384       # longest sequence (sizes graph block tables)
     max_num_seqs: int = 256          # concurrent running requests
     max_prefill_tokens: int = 16384  # chunked-prefill budget per step
-    schedule_policy: str = "fcfs"    # admission order: "fcfs" or "lpm" (longest cached prefix first)
+    schedule_policy: str = "fcfs"    # admission order: "fcfs", "lpm" (longest cached prefix first), "priority"
     mixed_steps: bool = False        # prefill steps also advance running requests by one decode token
     prefill_tail: bool = True        # window-only late layers (V4 family) run only on each prompt's tail rows
     kv_cache_fraction: float = 0.85  # of free HBM after weights

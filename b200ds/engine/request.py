@@ -23,6 +23,7 @@ class SamplingParams:
     repetition_penalty: float = 1.0  # prompt / output tokens: positive logits / r, negative * r
     min_p: float = 0.0              # drop tokens below min_p x the top probability (temperature > 0)
     min_tokens: int = 0             # no end-of-sequence / stop token before this many output tokens
+    priority: int = 0               # schedule_policy "priority": lower is admitted first
     prompt_logprobs: Optional[int] = None  # log-probability of every prompt token (+ top-n); computes the
                                            # whole prompt (no prefix-cache reuse)
 

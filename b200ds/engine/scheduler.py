@@ -43,12 +43,14 @@ LPM_MAX_QUEUE = 128
 class Scheduler:
     def __init__(self, pool: PagePool, max_num_seqs: int, max_prefill_tokens: int,
                  radix: Optional[RadixCache] = None, mixed: bool = False, policy: str = "fcfs"):
-        if policy not in ("fcfs", "lpm"):
-            raise ValueError(f"schedule policy {policy!r}: fcfs or lpm")
+        if policy not in ("fcfs", "lpm", "priority"):
+            raise ValueError(f"schedule policy {policy!r}: fcfs, lpm or priority")
         self.pool = pool
         # lpm: admit the waiting requests with the longest cached prefix first
         # (more prefix-cache hits before those pages are evicted); arrival
-        # order breaks ties, and queues longer than LPM_MAX_QUEUE stay FCFS
+        # order breaks ties, and queues longer than LPM_MAX_QUEUE stay FCFS.
+        # priority: lower SamplingParams.priority first, arrival order within
+        # a level (admission only: running requests are not preempted for it)
         self.policy = policy
         # mixed = True: a prefill step also carries one decode token of every
         # running request, so decoding does not stall behind long prompts
@@ -129,6 +131,8 @@ class Scheduler:
                 order = sorted(self.waiting, key=lambda r: -self.radix.match_len(
                     r.all_tokens[: prefill_target(r) - 1] if r.output else r.prompt[:-1]))
                 self.waiting = deque(order)
+            elif self.policy == "priority" and len(self.waiting) > 1:
+                self.waiting = deque(sorted(self.waiting, key=lambda r: r.params.priority))
             while self.waiting and len(self.running) + len(cands) < self.max_num_seqs:
                 r = self.waiting.popleft()
                 self._admit(r)

@@ -498,6 +498,7 @@ def _params(body: dict, default_max: int = 16, chat: bool = False) -> SamplingPa
         stop_token_ids=list(stop_ids),
         logprobs=_logprobs_param(body, chat),
         prompt_logprobs=(_logprobs_param(body, chat) if body.get("echo") and not chat else None),
+        priority=int(body.get("priority") or 0),
         **_penalty_params(body),
     )
 
@@ -748,8 +749,8 @@ def main(argv=None):
     ap.add_argument("--no-prefill-tail", action="store_true", help="window-only late layers on every prefill row")
     ap.add_argument("--host-kv-pages", type=int, default=0,
                     help="pinned host pages behind the prefix cache (evicted pages move there)")
-    ap.add_argument("--schedule-policy", choices=("fcfs", "lpm"), default="fcfs",
-                    help="admission order: arrival, or longest cached prefix first")
+    ap.add_argument("--schedule-policy", choices=("fcfs", "lpm", "priority"), default="fcfs",
+                    help="admission order: arrival, longest cached prefix first, or request priority")
     ap.add_argument("--comm", choices=("fused", "nccl"), default="fused",
                     help="fused NVLink collectives or the NCCL baseline")
     ap.add_argument("--watchdog-timeout", type=float, default=300.0,

@@ -358,3 +358,15 @@ def test_single_group_many_experts_matches_oracle():
     outs = eng.generate(prompts.tolist(), SamplingParams(max_tokens=5))
     toks, _ = ReferenceModel(cfg, sd).greedy(prompts, 5)
     assert [o.token_ids for o in outs] == toks.tolist()
+
+
+def test_priority_policy_admits_lower_priority_values_first():
+    pool = PagePool(64, 4)
+    s = Scheduler(pool, max_num_seqs=1, max_prefill_tokens=64, policy="priority")
+    a = Request(1, list(range(1, 9)), SamplingParams(priority=5))
+    b = Request(2, list(range(11, 19)), SamplingParams(priority=-1))
+    c = Request(3, list(range(21, 29)), SamplingParams(priority=5))
+    for r in (a, b, c):
+        s.add(r)
+    assert s.next_step().reqs == [b]
+    assert [r.rid for r in s.waiting] == [1, 3]          # arrival order within a level
