@@ -152,6 +152,14 @@ class Engine:
             raise ValueError(f"token id {bad!r} is outside the vocabulary [0, {V})")
         if params.max_tokens < 0:
             raise ValueError("max_tokens must be >= 0")
+        if params.guided_regex is not None or params.guided_choice:
+            if self.tokenizer is None:
+                raise ValueError("guided decoding needs a tokenizer")
+            from .guided import Guide, guide_pattern
+            try:
+                Guide(guide_pattern(params))
+            except Exception as e:
+                raise ValueError(f"guided pattern does not compile: {e}")
         total = n + params.max_tokens
         if total > self.ecfg.max_model_len:
             raise ValueError(f"the maximum context length is {self.ecfg.max_model_len} tokens; the request needs "
@@ -358,7 +366,7 @@ class Engine:
 
     def _sample(self, step: Step, logits: torch.Tensor) -> List[int]:
         if any(needs_adjust(r.params) for r in step.reqs):
-            logits = adjust_logits(logits, step.reqs, step.sample, self.eos)
+            logits = adjust_logits(logits, step.reqs, step.sample, self.eos, self.tokenizer)
         B = logits.shape[0]
         temp = torch.tensor([r.params.temperature for r in step.reqs], dtype=torch.float32)
         if bool((temp <= 0).all()):
@@ -408,8 +416,11 @@ class Engine:
         for r, smp, new in zip(st.reqs, st.sample, multi):
             if not smp:
                 continue
-            if r.params.max_tokens <= 0:      # prompt only (e.g. prompt log-probabilities): no token
-                r.finished, r.finish_reason, r.t_done = True, "length", now
+            if r.params.max_tokens <= 0 or getattr(r, "guide_done", False):
+                # prompt only (e.g. prompt log-probabilities), or a guided output
+                # that no token can extend: no token
+                r.finished, r.t_done = True, now
+                r.finish_reason = "stop" if r.params.max_tokens > 0 else "length"
                 self.sched.finish(r)
                 done.append(r)
                 continue

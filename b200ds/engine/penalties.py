@@ -10,7 +10,9 @@ full-vocabulary logits of the eager path before sampling:
     masked (logit -1e30) until the output holds n tokens;
   * min_p m: with temperature T > 0, tokens whose probability under
     softmax(logits / T) is below m times the largest are masked (greedy rows
-    are unaffected).
+    are unaffected);
+  * guided_regex / guided_choice: tokens that cannot extend the output to a
+    match are masked (engine/guided.py).
 
 Steps with such requests run the forward that returns logits instead of the
 token-only decode graph (the graph's on-device sampler has no per-request
@@ -29,13 +31,15 @@ MASKED = -1e30
 
 def needs_adjust(p) -> bool:
     return (p.presence_penalty != 0.0 or p.frequency_penalty != 0.0 or p.repetition_penalty != 1.0
-            or p.min_p > 0.0 or p.min_tokens > 0)
+            or p.min_p > 0.0 or p.min_tokens > 0 or p.guided_regex is not None or bool(p.guided_choice))
 
 
 def adjust_logits(logits: torch.Tensor, reqs: Sequence, sample: Optional[Sequence[bool]] = None,
-                  eos: Optional[int] = None) -> torch.Tensor:
+                  eos: Optional[int] = None, tokenizer=None) -> torch.Tensor:
     """A copy of logits [B, V] with row i adjusted for reqs[i] (rows whose
-    request needs nothing, or that do not sample this step, are unchanged)."""
+    request needs nothing, or that do not sample this step, are unchanged).
+    Guided requests (engine/guided.py) are masked last; one that cannot
+    continue gets `guide_done` set."""
     out = logits.float().clone()
     V = out.shape[1]
     dev = out.device
@@ -60,4 +64,8 @@ def adjust_logits(logits: torch.Tensor, reqs: Sequence, sample: Optional[Sequenc
         if p.min_p > 0.0 and p.temperature > 0:
             pr = (row / p.temperature).softmax(-1)
             row.masked_fill_(pr < p.min_p * pr.max(), MASKED)
+    if any(r.params.guided_regex is not None or r.params.guided_choice for r in reqs):
+        from .guided import apply_guides
+        for i in apply_guides(out, reqs, sample, tokenizer, eos, MASKED):
+            reqs[i].guide_done = True
     return out

@@ -24,6 +24,8 @@ class SamplingParams:
     min_p: float = 0.0              # drop tokens below min_p x the top probability (temperature > 0)
     min_tokens: int = 0             # no end-of-sequence / stop token before this many output tokens
     priority: int = 0               # schedule_policy "priority": lower is admitted first
+    guided_regex: Optional[str] = None        # the output text must match this regular expression
+    guided_choice: Optional[List[str]] = None  # ... or be one of these strings
     prompt_logprobs: Optional[int] = None  # log-probability of every prompt token (+ top-n); computes the
                                            # whole prompt (no prefix-cache reuse)
 

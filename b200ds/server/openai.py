@@ -499,6 +499,8 @@ def _params(body: dict, default_max: int = 16, chat: bool = False) -> SamplingPa
         logprobs=_logprobs_param(body, chat),
         prompt_logprobs=(_logprobs_param(body, chat) if body.get("echo") and not chat else None),
         priority=int(body.get("priority") or 0),
+        guided_regex=body.get("guided_regex", body.get("regex")),
+        guided_choice=body.get("guided_choice"),
         **_penalty_params(body),
     )
 

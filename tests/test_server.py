@@ -299,3 +299,14 @@ def test_worker_refuses_a_bad_request_without_failing():
     worker.stop()
     assert bad.items and bad.items[0][0] == "error" and "empty" in bad.items[0][1]
     assert worker.healthy() and any(ev[0] == "done" for ev in good.items)
+
+
+def test_guided_fields(client):
+    r = client.post("/v1/completions", json={"prompt": "answer:", "max_tokens": 8, "temperature": 0,
+                                             "guided_choice": ["left", "right"]}).json()
+    assert r["choices"][0]["text"] in ("left", "right")
+    r = client.post("/v1/completions", json={"prompt": "id:", "max_tokens": 8, "temperature": 0.7, "seed": 2,
+                                             "regex": "[0-9]{4}"}).json()
+    t = r["choices"][0]["text"]
+    assert len(t) == 4 and t.isdigit()
+    assert client.post("/v1/completions", json={"prompt": "x", "guided_regex": "("}).status_code == 400
