@@ -152,7 +152,7 @@ class Engine:
             raise ValueError(f"token id {bad!r} is outside the vocabulary [0, {V})")
         if params.max_tokens < 0:
             raise ValueError("max_tokens must be >= 0")
-        if params.guided_regex is not None or params.guided_choice:
+        if params.guided_regex is not None or params.guided_choice or params.guided_json is not None:
             if self.tokenizer is None:
                 raise ValueError("guided decoding needs a tokenizer")
             from .guided import Guide, guide_pattern

@@ -27,6 +27,8 @@ def guide_pattern(p) -> Optional[str]:
         return p.guided_regex
     if p.guided_choice:
         return "(?:" + "|".join(re.escape(c) for c in p.guided_choice) + ")"
+    if p.guided_json is not None:
+        return JSON_OBJECT if p.guided_json == "object" else schema_to_regex(p.guided_json)
     return None
 
 
@@ -95,3 +97,74 @@ def apply_guides(logits: torch.Tensor, reqs, sample, tokenizer, eos: Optional[in
             continue
         logits[i].masked_fill_(~m.to(logits.device), masked)
     return ended
+
+
+# ---------------------------------------------------------------------------
+# JSON schema -> regular expression (a practical subset)
+# ---------------------------------------------------------------------------
+
+_WS = "[ ]?"
+_STR_CH = r'(?:[^"\\\x00-\x1f]|\\["\\/bfnrt])'
+_INT = r"-?(?:0|[1-9][0-9]{0,17})"
+_NUM = _INT + r"(?:\.[0-9]{1,17})?(?:[eE][+-]?[0-9]{1,3})?"
+
+
+def schema_to_regex(schema: dict) -> str:
+    """Regular expression of the compact JSON texts a schema accepts, for
+    this subset: type string (maxLength / minLength, enum, const), integer,
+    number, boolean, null; object with properties (emitted in declaration
+    order, all present); array with items (minItems / maxItems); enum,
+    const, anyOf / oneOf.  Numbers are bounded to 18 digits so a guided
+    output always reaches its end.  Anything else raises ValueError."""
+    import json
+    if not isinstance(schema, dict):
+        raise ValueError("schema must be an object")
+    for k in ("enum", "const"):
+        if k in schema:
+            vals = schema[k] if k == "enum" else [schema[k]]
+            return "(?:" + "|".join(re.escape(json.dumps(v, separators=(",", ":"))) for v in vals) + ")"
+    for k in ("anyOf", "oneOf"):
+        if k in schema:
+            return "(?:" + "|".join(schema_to_regex(s) for s in schema[k]) + ")"
+    t = schema.get("type")
+    if isinstance(t, list):
+        return "(?:" + "|".join(schema_to_regex(dict(schema, type=x)) for x in t) + ")"
+    if t == "string":
+        lo, hi = int(schema.get("minLength", 0)), schema.get("maxLength")
+        return '"' + _STR_CH + ("{%d,%d}" % (lo, int(hi)) if hi is not None else ("{%d,}" % lo if lo else "*")) + '"'
+    if t == "integer":
+        return _INT
+    if t == "number":
+        return _NUM
+    if t == "boolean":
+        return "(?:true|false)"
+    if t == "null":
+        return "null"
+    if t == "object":
+        props = schema.get("properties") or {}
+        if not props:
+            return r"\{" + _WS + r"\}"
+        parts = [re.escape(json.dumps(k)) + _WS + ":" + _WS + schema_to_regex(v) for k, v in props.items()]
+        return r"\{" + _WS + ("," + _WS).join(parts) + _WS + r"\}"
+    if t == "array":
+        item = schema_to_regex(schema.get("items") or {"type": "string", "maxLength": 64})
+        lo, hi = int(schema.get("minItems", 0)), schema.get("maxItems")
+        more = "(?:," + _WS + item + ")"
+        if hi is not None:
+            hi = int(hi)
+            body = "" if hi == 0 else item + more + "{%d,%d}" % (max(lo - 1, 0), hi - 1)
+            opt = lo == 0 and hi > 0
+        else:
+            body = item + more + ("{%d,}" % (lo - 1) if lo > 1 else "*")
+            opt = lo == 0
+        inner = ("(?:" + body + ")?") if opt else body
+        return r"\[" + _WS + inner + _WS + r"\]"
+    raise ValueError(f"unsupported schema: {json.dumps(schema)[:80]}")
+
+
+# response_format {"type": "json_object"}: a flat JSON object (string keys of
+# up to 64 characters, primitive values)
+_KEY = '"' + _STR_CH + '{1,64}"'
+_PRIM = "(?:" + '"' + _STR_CH + '{0,256}"' + "|" + _NUM + "|true|false|null)"
+_PAIR = _KEY + _WS + ":" + _WS + _PRIM
+JSON_OBJECT = r"\{" + _WS + "(?:" + _PAIR + "(?:," + _WS + _PAIR + "){0,63})?" + _WS + r"\}"

@@ -31,7 +31,8 @@ MASKED = -1e30
 
 def needs_adjust(p) -> bool:
     return (p.presence_penalty != 0.0 or p.frequency_penalty != 0.0 or p.repetition_penalty != 1.0
-            or p.min_p > 0.0 or p.min_tokens > 0 or p.guided_regex is not None or bool(p.guided_choice))
+            or p.min_p > 0.0 or p.min_tokens > 0 or p.guided_regex is not None or bool(p.guided_choice)
+            or p.guided_json is not None)
 
 
 def adjust_logits(logits: torch.Tensor, reqs: Sequence, sample: Optional[Sequence[bool]] = None,
@@ -64,7 +65,8 @@ def adjust_logits(logits: torch.Tensor, reqs: Sequence, sample: Optional[Sequenc
         if p.min_p > 0.0 and p.temperature > 0:
             pr = (row / p.temperature).softmax(-1)
             row.masked_fill_(pr < p.min_p * pr.max(), MASKED)
-    if any(r.params.guided_regex is not None or r.params.guided_choice for r in reqs):
+    if any(r.params.guided_regex is not None or r.params.guided_choice or r.params.guided_json is not None
+           for r in reqs):
         from .guided import apply_guides
         for i in apply_guides(out, reqs, sample, tokenizer, eos, MASKED):
             reqs[i].guide_done = True

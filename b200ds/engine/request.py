@@ -26,6 +26,7 @@ class SamplingParams:
     priority: int = 0               # schedule_policy "priority": lower is admitted first
     guided_regex: Optional[str] = None        # the output text must match this regular expression
     guided_choice: Optional[List[str]] = None  # ... or be one of these strings
+    guided_json: Optional[object] = None       # ... or be JSON matching this schema ("object": any flat object)
     prompt_logprobs: Optional[int] = None  # log-probability of every prompt token (+ top-n); computes the
                                            # whole prompt (no prefix-cache reuse)
 

@@ -443,6 +443,19 @@ def _max_tokens(body: dict, default: int) -> int:
     return v
 
 
+def _json_guide(body: dict):
+    """guided_json (a schema) or response_format json_schema / json_object."""
+    if body.get("guided_json") is not None:
+        return body["guided_json"]
+    rf = body.get("response_format") or {}
+    if rf.get("type") == "json_schema":
+        js = rf.get("json_schema") or {}
+        return js.get("schema", js)
+    if rf.get("type") == "json_object":
+        return "object"
+    return None
+
+
 def _penalty_params(body: dict) -> dict:
     """presence_penalty / frequency_penalty (OpenAI, -2..2), repetition_penalty
     (> 0), min_p (0..1), min_tokens (>= 0)."""
@@ -501,6 +514,7 @@ def _params(body: dict, default_max: int = 16, chat: bool = False) -> SamplingPa
         priority=int(body.get("priority") or 0),
         guided_regex=body.get("guided_regex", body.get("regex")),
         guided_choice=body.get("guided_choice"),
+        guided_json=_json_guide(body),
         **_penalty_params(body),
     )
 

@@ -45,3 +45,26 @@ def test_guided_with_eos_and_validation():
     bare.tokenizer = None
     with pytest.raises(ValueError):
         bare.add_request([5], SamplingParams(guided_choice=["a"]))
+
+
+def test_guided_json_schema_and_object():
+    import json
+    from b200ds.engine.guided import schema_to_regex
+    eng, tok = _engine()
+    schema = {"type": "object", "properties": {"name": {"type": "string", "maxLength": 4},
+                                               "n": {"type": "integer"}, "ok": {"type": "boolean"},
+                                               "tags": {"type": "array", "items": {"enum": ["a", "b"]},
+                                                        "maxItems": 2}}}
+    for seed in range(3):
+        o = eng.generate([tok.encode("json:")], SamplingParams(max_tokens=80, temperature=0.9, seed=seed,
+                                                               guided_json=schema))[0]
+        d = json.loads(tok.decode(o.token_ids))
+        assert list(d) == ["name", "n", "ok", "tags"] and len(d["name"]) <= 4 and isinstance(d["n"], int)
+        assert isinstance(d["ok"], bool) and set(d["tags"]) <= {"a", "b"} and len(d["tags"]) <= 2
+    o = eng.generate([tok.encode("obj:")], SamplingParams(max_tokens=60, guided_json="object"))[0]
+    text = tok.decode(o.token_ids)
+    assert text.startswith("{")
+    if o.finish_reason == "stop":
+        assert isinstance(json.loads(text), dict)
+    with pytest.raises(ValueError):
+        schema_to_regex({"type": "object", "properties": {"x": {"$ref": "#/defs/y"}}})

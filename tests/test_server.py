@@ -310,3 +310,14 @@ def test_guided_fields(client):
     t = r["choices"][0]["text"]
     assert len(t) == 4 and t.isdigit()
     assert client.post("/v1/completions", json={"prompt": "x", "guided_regex": "("}).status_code == 400
+
+
+def test_response_format_json_schema(client):
+    schema = {"type": "object", "properties": {"k": {"type": "integer"}, "v": {"enum": ["x", "y"]}}}
+    r = client.post("/v1/chat/completions", json={
+        "messages": [{"role": "user", "content": "json"}], "max_tokens": 40, "temperature": 0,
+        "response_format": {"type": "json_schema", "json_schema": {"name": "t", "schema": schema}}}).json()
+    d = json.loads(r["choices"][0]["message"]["content"])
+    assert list(d) == ["k", "v"] and isinstance(d["k"], int) and d["v"] in ("x", "y")
+    bad = client.post("/v1/completions", json={"prompt": "x", "guided_json": {"type": "tuple"}})
+    assert bad.status_code == 400
