@@ -691,6 +691,32 @@ class Engine:
         self._mtp_chain(st.reqs, draft, hid, [n + len(o) + 1 for o, n in zip(out, st.starts)])
         return out
 
+    def update_weights(self, weights, seed: int = 0) -> int:
+        """Load new weights of the same architecture (a checkpoint directory,
+        a full state dict, or "random" with a seed) into the live model in
+        place; returns the bytes copied.  Captured graphs stay valid (same
+        buffers); the prefix cache, whose rows came from the old weights, is
+        cleared.  Call with no requests in flight; every rank of an SPMD job
+        makes the same call."""
+        if self.sched.has_work:
+            raise ValueError("update_weights needs an idle engine (no queued or running requests)")
+        from .. import build_model_from
+        from ..models.weights_update import copy_weights
+        new = build_model_from(self.cfg, self.ecfg, weights, device=self.device, seed=seed, ps=self.ps)
+        n = copy_weights(self.model, new)
+        del new
+        self.flush_cache()
+        return n
+
+    def flush_cache(self) -> int:
+        """Clear the prefix cache (both tiers); returns the device pages
+        freed.  Only when no request holds cached pages (an idle engine)."""
+        if self.radix is None:
+            return 0
+        if self.sched.has_work:
+            raise ValueError("flush_cache needs an idle engine")
+        return self.radix.clear()
+
     def gauges(self) -> Dict[str, float]:
         """Current queue and KV-pool state and the scheduler's counters."""
         sc = self.sched

@@ -168,6 +168,23 @@ class RadixCache:
             self.num_nodes -= 1
         del n.parent.children[n.key]
 
+    def clear(self) -> int:
+        """Drop every node (none may be locked); returns the device pages
+        released."""
+        freed = 0
+        for n in list(self._iter()):
+            if n is self.root:
+                continue
+            assert n.locks == 0, "clear() with a locked prefix"
+            if n.page >= 0:
+                self.pool.release([n.page])
+                freed += 1
+            elif n.host_page >= 0:
+                self.host.free(n.host_page)
+        self.root.children = {}
+        self.num_nodes = 0
+        return freed
+
     def _iter(self):
         stack = [self.root]
         while stack:

@@ -49,6 +49,8 @@ class EngineWorker:
             self.watchdog = Watchdog(watchdog_s, exit_code=70 if watchdog_exit else None)
         self.inbox: "queue.Queue" = queue.Queue()
         self.cancels: "queue.Queue" = queue.Queue()     # subscription queues whose client went away
+        self.commands: "queue.Queue" = queue.Queue()    # weight updates (path, loop, q)
+        self.pending_update = None
         self.subs: Dict[int, tuple] = {}     # rid -> (loop, asyncio.Queue, emitted count)
         self._stop = threading.Event()
         self.t = threading.Thread(target=self._run, daemon=True)
@@ -79,6 +81,25 @@ class EngineWorker:
             _post(loop, q, ("error", self.error))
             return
         self.inbox.put((prompt_ids, params, loop, q))
+
+    def request_update(self, path: str, loop, q) -> None:
+        """Queue a weight update: admission pauses, the update runs on every
+        rank once no request is in flight, the result is posted to q."""
+        self.commands.put((path, loop, q))
+
+    def _update_due(self) -> bool:
+        """Pick up a queued update; True when one is pending and nothing is in flight."""
+        if self.pending_update is None:
+            try:
+                self.pending_update = self.commands.get_nowait()
+            except queue.Empty:
+                return False
+        return not self.subs and not self.engine.sched.has_work
+
+    def _run_update(self) -> None:
+        path, loop, q = self.pending_update
+        self.pending_update = None
+        _post(loop, q, _apply_update(self.engine, path))
 
     def _step(self):
         """One engine step under the watchdog (when configured)."""
@@ -138,8 +159,13 @@ class EngineWorker:
     def _loop(self):
         eng = self.engine
         while not self._stop.is_set():
+            if self._update_due():
+                if self.ps is not None and self.ps.world_size > 1:
+                    _broadcast_requests(self.ps, {"new": [], "abort": [], "update": self.pending_update[0]})
+                self._run_update()
+                continue
             new = []
-            for prompt, params, loop, q in self._admit():
+            for prompt, params, loop, q in (self._admit() if self.pending_update is None else []):
                 try:
                     r = eng.add_request(prompt, params)
                 except ValueError as e:        # refused before it is queued (and never broadcast)
@@ -180,6 +206,14 @@ class EngineWorker:
             _broadcast_requests(self.ps, None)      # followers stop
 
 
+def _apply_update(engine, path: str) -> tuple:
+    """engine.update_weights on this rank; ("updated", bytes) or ("error", why)."""
+    try:
+        return ("updated", engine.update_weights(path))
+    except (ValueError, OSError, KeyError) as e:
+        return ("error", f"{type(e).__name__}: {e}")
+
+
 def _post(loop, q, item) -> bool:
     """Hand an event to a request handler's event loop; False when that loop
     has closed (the client is gone)."""
@@ -213,7 +247,11 @@ class DPEngineWorker(EngineWorker):
         eng, ps = self.engine, self.ps
         world = ps.world_size
         while not self._stop.is_set():
-            new = self._admit()
+            if self._update_due():
+                _broadcast_requests(ps, {"new": [], "abort": [], "update": self.pending_update[0]})
+                self._run_update()
+                continue
+            new = self._admit() if self.pending_update is None else []
             batch = []
             for prompt, params, loop, q in new:
                 try:
@@ -314,6 +352,9 @@ def dp_follower_loop(engine, ps) -> None:
         msg = _broadcast_requests(ps, None)
         if msg is None:
             return
+        if msg.get("update"):
+            _apply_update(engine, msg["update"])
+            continue
         _dp_admit(engine, ps, msg["new"], own)
         _dp_abort(engine, msg["abort"], own)
         engine.step()
@@ -330,6 +371,9 @@ def follower_loop(engine, ps) -> None:
         msg = _broadcast_requests(ps, None)
         if msg is None:
             return
+        if msg.get("update"):
+            _apply_update(engine, msg["update"])
+            continue
         for prompt, spd in msg["new"]:
             r = engine.add_request(prompt, SamplingParams(**spd))
             reqs_by_rid[r.rid] = r
@@ -710,6 +754,22 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
     @app.get("/v1/models")
     async def models():
         return {"object": "list", "data": [{"id": model_name, "object": "model", "owned_by": "b200ds"}]}
+
+    @app.post("/update_weights_from_disk")
+    async def update_weights(request: Request):
+        """{"model_path": checkpoint dir}: new weights of the same architecture,
+        loaded in place once the requests in flight have finished."""
+        body = await request.json()
+        path = body.get("model_path")
+        if not isinstance(path, str):
+            raise HTTPException(400, "model_path must be a checkpoint directory")
+        loop = asyncio.get_running_loop()
+        q: asyncio.Queue = asyncio.Queue()
+        worker.request_update(path, loop, q)
+        kind, val = await q.get()
+        if kind == "error":
+            raise HTTPException(400, val)
+        return {"success": True, "bytes": int(val)}
 
     @app.post("/tokenize")
     async def tokenize(request: Request):

@@ -321,3 +321,27 @@ def test_response_format_json_schema(client):
     assert list(d) == ["k", "v"] and isinstance(d["k"], int) and d["v"] in ("x", "y")
     bad = client.post("/v1/completions", json={"prompt": "x", "guided_json": {"type": "tuple"}})
     assert bad.status_code == 400
+
+
+def test_update_weights_from_disk(tmp_path):
+    """POST /update_weights_from_disk loads a checkpoint of the same
+    architecture in place; later completions follow the new weights."""
+    from b200ds import EngineConfig, load_engine
+    from b200ds.config import tiny_config
+    from b200ds.models.loader import save_checkpoint_fp8
+    from b200ds.models.reference import init_weights
+    cfg = tiny_config()
+    save_checkpoint_fp8(init_weights(cfg, 5), str(tmp_path), cfg)
+    want = load_engine(str(tmp_path), ecfg=EngineConfig(page_size=8, cuda_graphs=False), device="cpu").generate(
+        [[7, 8, 9]], __import__("b200ds").SamplingParams(max_tokens=4))[0].token_ids
+    eng, worker, client = _fresh_client()
+    worker.start()
+    with client as c:
+        before = c.post("/v1/completions", json={"prompt": [7, 8, 9], "max_tokens": 4, "temperature": 0}).json()
+        r = c.post("/update_weights_from_disk", json={"model_path": str(tmp_path)})
+        assert r.status_code == 200 and r.json()["success"] and r.json()["bytes"] > 0
+        after = c.post("/v1/completions", json={"prompt": [7, 8, 9], "max_tokens": 4, "temperature": 0}).json()
+        assert after["choices"][0]["token_ids"] == want != before["choices"][0]["token_ids"]
+        bad = c.post("/update_weights_from_disk", json={"model_path": str(tmp_path / "missing")})
+        assert bad.status_code == 400 and c.get("/health").status_code == 200
+    worker.stop()
