@@ -27,6 +27,12 @@ def _generate(argv) -> int:
     ap.add_argument("--top-p", type=float, default=1.0)
     ap.add_argument("--top-k", type=int, default=0)
     ap.add_argument("--seed", type=int, default=None)
+    ap.add_argument("--logprobs", type=int, default=None, help="report each token's log-probability (+ top-n)")
+    ap.add_argument("--presence-penalty", type=float, default=0.0)
+    ap.add_argument("--frequency-penalty", type=float, default=0.0)
+    ap.add_argument("--repetition-penalty", type=float, default=1.0)
+    ap.add_argument("--guided-regex", default=None, help="constrain the output to this regular expression")
+    ap.add_argument("--guided-choice", default=None, help="comma-separated allowed outputs")
     ap.add_argument("--device", default=None)
     ap.add_argument("--no-cuda-graphs", action="store_true")
     a = ap.parse_args(argv)
@@ -37,13 +43,19 @@ def _generate(argv) -> int:
     ecfg = EngineConfig(tp_size=ps.tp_size, ep_size=ps.ep_size, cuda_graphs=not a.no_cuda_graphs)
     eng = load_engine(a.model, weights=a.weights, ecfg=ecfg, device=a.device)
     tok = load_tokenizer(a.model)
+    eng.tokenizer = eng.tokenizer or tok
     ids = [int(x) for x in a.ids.split(",")] if a.ids else tok.encode(a.prompt or "Hello")
     sp = SamplingParams(max_tokens=a.max_tokens, temperature=a.temperature, top_p=a.top_p, top_k=a.top_k,
-                        seed=a.seed)
+                        seed=a.seed, logprobs=a.logprobs, presence_penalty=a.presence_penalty,
+                        frequency_penalty=a.frequency_penalty, repetition_penalty=a.repetition_penalty,
+                        guided_regex=a.guided_regex,
+                        guided_choice=a.guided_choice.split(",") if a.guided_choice else None)
     out = eng.generate([ids], sp)[0]
     if ps.rank == 0:
-        print(json.dumps({"token_ids": out.token_ids, "text": tok.decode(out.token_ids),
-                          "finish_reason": out.finish_reason}))
+        res = {"token_ids": out.token_ids, "text": tok.decode(out.token_ids), "finish_reason": out.finish_reason}
+        if out.logprobs is not None:
+            res["logprobs"] = [lp for _, lp, _ in out.logprobs]
+        print(json.dumps(res))
     return 0
 
 

@@ -771,6 +771,16 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
             raise HTTPException(400, val)
         return {"success": True, "bytes": int(val)}
 
+    @app.post("/flush_cache")
+    async def flush_cache():
+        """Clear the prefix cache when no request is in flight (409 otherwise)."""
+        if worker.subs or worker.engine.sched.has_work:
+            raise HTTPException(409, "requests are in flight")
+        try:
+            return {"success": True, "pages": worker.engine.flush_cache()}
+        except ValueError as e:
+            raise HTTPException(409, str(e))
+
     @app.post("/tokenize")
     async def tokenize(request: Request):
         """{"prompt": text} or {"messages": [...]} -> token ids (chat template applied)."""

@@ -26,3 +26,11 @@ def test_generate_tiny_cpu():
     assert p.returncode == 0, p.stderr
     out = json.loads(p.stdout.strip().splitlines()[-1])
     assert len(out["token_ids"]) == 3 and out["finish_reason"] == "length"
+
+
+def test_generate_guided_with_logprobs():
+    p = _run("generate", "--model", "tiny", "--device", "cpu", "--no-cuda-graphs", "--prompt", "pick",
+             "--max-tokens", "8", "--guided-choice", "red,green", "--logprobs", "0")
+    assert p.returncode == 0, p.stderr
+    out = json.loads(p.stdout.strip().splitlines()[-1])
+    assert out["text"] in ("red", "green") and len(out["logprobs"]) == len(out["token_ids"])

@@ -345,3 +345,9 @@ def test_update_weights_from_disk(tmp_path):
         bad = c.post("/update_weights_from_disk", json={"model_path": str(tmp_path / "missing")})
         assert bad.status_code == 400 and c.get("/health").status_code == 200
     worker.stop()
+
+
+def test_flush_cache_endpoint(client):
+    client.post("/v1/completions", json={"prompt": list(range(3, 40)), "max_tokens": 2, "temperature": 0})
+    r = client.post("/flush_cache")
+    assert r.status_code == 200 and r.json()["success"] and r.json()["pages"] > 0
