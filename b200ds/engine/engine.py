@@ -152,6 +152,8 @@ class Engine:
             raise ValueError(f"token id {bad!r} is outside the vocabulary [0, {V})")
         if params.max_tokens < 0:
             raise ValueError("max_tokens must be >= 0")
+        if params.logit_bias and any(not 0 <= int(t) < V for t in params.logit_bias):
+            raise ValueError("logit_bias names a token id outside the vocabulary")
         if params.guided_regex is not None or params.guided_choice or params.guided_json is not None:
             if self.tokenizer is None:
                 raise ValueError("guided decoding needs a tokenizer")

@@ -1,6 +1,7 @@
 """Logit adjustments requested per sampling request, applied to the
 full-vocabulary logits of the eager path before sampling:
 
+  * logit_bias {token: b} (OpenAI form): b is added to that token's logit;
   * repetition_penalty r (CTRL / HF form): every token already in the prompt
     or the output has its logit divided by r when positive, multiplied by r
     when negative;
@@ -32,7 +33,7 @@ MASKED = -1e30
 def needs_adjust(p) -> bool:
     return (p.presence_penalty != 0.0 or p.frequency_penalty != 0.0 or p.repetition_penalty != 1.0
             or p.min_p > 0.0 or p.min_tokens > 0 or p.guided_regex is not None or bool(p.guided_choice)
-            or p.guided_json is not None)
+            or p.guided_json is not None or bool(p.logit_bias))
 
 
 def adjust_logits(logits: torch.Tensor, reqs: Sequence, sample: Optional[Sequence[bool]] = None,
@@ -49,6 +50,9 @@ def adjust_logits(logits: torch.Tensor, reqs: Sequence, sample: Optional[Sequenc
         if not needs_adjust(p) or (sample is not None and not sample[i]):
             continue
         row = out[i]
+        if p.logit_bias:
+            ids = torch.tensor([int(t) for t in p.logit_bias], dtype=torch.long, device=dev)
+            row[ids] += torch.tensor([float(v) for v in p.logit_bias.values()], dtype=row.dtype, device=dev)
         if p.repetition_penalty != 1.0:
             seen = torch.tensor(sorted(set(r.prompt) | set(r.output)), dtype=torch.long, device=dev)
             if seen.numel():

@@ -24,6 +24,7 @@ class SamplingParams:
     min_p: float = 0.0              # drop tokens below min_p x the top probability (temperature > 0)
     min_tokens: int = 0             # no end-of-sequence / stop token before this many output tokens
     priority: int = 0               # schedule_policy "priority": lower is admitted first
+    logit_bias: Optional[dict] = None  # token id -> value added to its logit (OpenAI logit_bias)
     guided_regex: Optional[str] = None        # the output text must match this regular expression
     guided_choice: Optional[List[str]] = None  # ... or be one of these strings
     guided_json: Optional[object] = None       # ... or be JSON matching this schema ("object": any flat object)

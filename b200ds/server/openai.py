@@ -487,6 +487,22 @@ def _max_tokens(body: dict, default: int) -> int:
     return v
 
 
+def _logit_bias(body: dict):
+    """OpenAI logit_bias: {token id (string or int): bias in [-100, 100]}."""
+    lb = body.get("logit_bias")
+    if not lb:
+        return None
+    if not isinstance(lb, dict):
+        raise ValueError("logit_bias must map token ids to biases")
+    out = {}
+    for k, v in lb.items():
+        v = float(v)
+        if not -100.0 <= v <= 100.0:
+            raise ValueError("logit_bias values must be in [-100, 100]")
+        out[int(k)] = v
+    return out
+
+
 def _json_guide(body: dict):
     """guided_json (a schema) or response_format json_schema / json_object."""
     if body.get("guided_json") is not None:
@@ -556,6 +572,7 @@ def _params(body: dict, default_max: int = 16, chat: bool = False) -> SamplingPa
         logprobs=_logprobs_param(body, chat),
         prompt_logprobs=(_logprobs_param(body, chat) if body.get("echo") and not chat else None),
         priority=int(body.get("priority") or 0),
+        logit_bias=_logit_bias(body),
         guided_regex=body.get("guided_regex", body.get("regex")),
         guided_choice=body.get("guided_choice"),
         guided_json=_json_guide(body),

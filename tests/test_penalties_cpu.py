@@ -75,3 +75,13 @@ def test_engine_presence_penalty_and_min_tokens():
     again = eng.generate([base], SamplingParams(max_tokens=24, presence_penalty=2.0, frequency_penalty=2.0,
                                                 repetition_penalty=1.5))[0].token_ids
     assert again == pen
+
+
+def test_logit_bias():
+    from b200ds.engine.penalties import adjust_logits
+    lg = torch.zeros(1, 10)
+    out = adjust_logits(lg, [_req([1], [], logit_bias={3: 5.0, 7: -100.0})])[0]
+    assert out[3] == 5.0 and out[7] == -100.0 and out[0] == 0.0
+    eng = _engine()
+    forced = eng.generate([[5, 6, 7]], SamplingParams(max_tokens=4, logit_bias={42: 100.0}))[0].token_ids
+    assert forced == [42] * 4

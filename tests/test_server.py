@@ -351,3 +351,10 @@ def test_flush_cache_endpoint(client):
     client.post("/v1/completions", json={"prompt": list(range(3, 40)), "max_tokens": 2, "temperature": 0})
     r = client.post("/flush_cache")
     assert r.status_code == 200 and r.json()["success"] and r.json()["pages"] > 0
+
+
+def test_logit_bias_field(client):
+    r = client.post("/v1/completions", json={"prompt": [5, 6], "max_tokens": 3, "temperature": 0,
+                                             "logit_bias": {"77": 100}}).json()
+    assert r["choices"][0]["token_ids"] == [77, 77, 77]
+    assert client.post("/v1/completions", json={"prompt": [5], "logit_bias": {"5": 1000}}).status_code == 400
