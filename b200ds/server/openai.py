@@ -657,8 +657,8 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
         rid = f"{'chatcmpl' if chat else 'cmpl'}-{uuid.uuid4().hex[:16]}"
         created = int(time.time())
         n = int(body.get("n") or 1)
-        if n < 1 or (n > 1 and body.get("stream")):
-            raise HTTPException(400, "n must be >= 1 (and 1 when streaming)")
+        if n < 1:
+            raise HTTPException(400, "n must be >= 1")
         obj = "chat.completion" if chat else "text_completion"
         stops = body.get("stop") or []
         stops = [stops] if isinstance(stops, str) else [x for x in stops if isinstance(x, str) and x]
@@ -673,7 +673,7 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
             if params.logprobs is not None:
                 c["logprobs"] = _lp_json(tok, lps, chat, prompt=(ids, plp) if echo else None)
             return c
-        if n > 1:
+        if n > 1 and not body.get("stream"):
             # n independent samples of the prompt (seed + i when a seed is given)
             import dataclasses
             qs = [await _run(ids, dataclasses.replace(params, seed=None if params.seed is None else params.seed + i))
@@ -684,75 +684,98 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
             return JSONResponse({"id": rid, "object": obj, "created": created, "model": model_name,
                                  "choices": choices, "usage": {"prompt_tokens": len(ids), "completion_tokens": gen_tok,
                                                                "total_tokens": len(ids) + gen_tok}})
-        q = await _run(ids, params)
         if body.get("stream"):
-            async def gen():
-                done = False
-                try:
-                    async for chunk in _chunks():
-                        yield chunk
-                    done = True
-                finally:
-                    if not done:              # client disconnected: free the request
-                        worker.cancel(q)
-
+            import dataclasses
+            qs = [await _run(ids, params if n == 1 else dataclasses.replace(
+                params, seed=None if params.seed is None else params.seed + i)) for i in range(n)]
+            counts = [0] * n
             usage = bool((body.get("stream_options") or {}).get("include_usage"))
 
-            def _final(n_out: int) -> str:
+            def _final() -> str:
                 """Closing events: the usage chunk (stream_options.include_usage)
                 and [DONE]."""
                 tail = "data: [DONE]\n\n"
                 if not usage:
                     return tail
+                n_out = sum(counts)
                 u = {"prompt_tokens": len(ids), "completion_tokens": n_out, "total_tokens": len(ids) + n_out}
                 ev = {"id": rid, "object": obj + ".chunk", "created": created, "model": model_name,
                       "choices": [], "usage": u}
                 return f"data: {json.dumps(ev)}\n\n" + tail
 
-            async def _chunks():
+            def _ev(choice) -> str:
+                return f"data: {json.dumps({'id': rid, 'object': obj + '.chunk', 'created': created, 'model': model_name, 'choices': [choice]})}\n\n"
+
+            async def _chunks(q, idx):
+                """Events of choice idx until it finishes."""
                 ids_all: List[int] = []
                 sent = 0                      # characters of the decoded text already streamed
                 if echo:                      # the prompt's text first
-                    ev0 = {"id": rid, "object": obj + ".chunk", "created": created, "model": model_name,
-                           "choices": [{"index": 0, "text": tok.decode(ids), "token_ids": [], "finish_reason": None}]}
-                    yield f"data: {json.dumps(ev0)}\n\n"
+                    yield _ev({"index": idx, "text": tok.decode(ids), "token_ids": [], "finish_reason": None})
                 while True:
                     ev = await q.get()
                     kind, val = ev[0], ev[1]
                     if kind == "error":
                         yield f"data: {json.dumps({'error': {'message': f'engine error: {val}', 'type': 'server_error'}})}\n\n"
-                        yield _final(len(ids_all))
                         return
                     if kind == "tokens":
                         lp_field = None
                         if params.logprobs is not None and len(ev) > 2 and ev[2]:
                             lp_field = _lp_json(tok, ev[2], chat, len(tok.decode(ids_all)))
                         ids_all.extend(val)
+                        counts[idx] = len(ids_all)
                         full = tok.decode(ids_all)
                         cut, hold = _stop_scan(full, stops)
                         end = cut if cut is not None else len(full) - hold
                         text = full[sent:end] if end > sent else ""
                         sent = max(sent, end)
                         if text or cut is None:
-                            choice = ({"index": 0, "delta": {"content": text}, "finish_reason": None} if chat
-                                      else {"index": 0, "text": text, "token_ids": val, "finish_reason": None})
+                            choice = ({"index": idx, "delta": {"content": text}, "finish_reason": None} if chat
+                                      else {"index": idx, "text": text, "token_ids": val, "finish_reason": None})
                             if lp_field is not None:
                                 choice["logprobs"] = lp_field
-                            yield f"data: {json.dumps({'id': rid, 'object': obj + '.chunk', 'created': created, 'model': model_name, 'choices': [choice]})}\n\n"
+                            yield _ev(choice)
                         if cut is not None:     # a stop string: finish now and free the request
                             worker.cancel(q)
-                            choice = ({"index": 0, "delta": {}, "finish_reason": "stop"} if chat
-                                      else {"index": 0, "text": "", "finish_reason": "stop"})
-                            yield f"data: {json.dumps({'id': rid, 'object': obj + '.chunk', 'created': created, 'model': model_name, 'choices': [choice]})}\n\n"
-                            yield _final(len(ids_all))
+                            yield _ev({"index": idx, "delta": {}, "finish_reason": "stop"} if chat
+                                      else {"index": idx, "text": "", "finish_reason": "stop"})
                             return
                     else:
-                        choice = ({"index": 0, "delta": {}, "finish_reason": val} if chat
-                                  else {"index": 0, "text": "", "finish_reason": val})
-                        yield f"data: {json.dumps({'id': rid, 'object': obj + '.chunk', 'created': created, 'model': model_name, 'choices': [choice]})}\n\n"
-                        yield _final(len(ids_all))
+                        yield _ev({"index": idx, "delta": {}, "finish_reason": val} if chat
+                                  else {"index": idx, "text": "", "finish_reason": val})
                         return
+
+            async def gen():
+                finished = [False] * n
+                try:
+                    if n == 1:
+                        async for chunk in _chunks(qs[0], 0):
+                            yield chunk
+                        finished[0] = True
+                    else:                     # the choices' events interleaved as they come
+                        merged: asyncio.Queue = asyncio.Queue()
+
+                        async def pump(i):
+                            async for chunk in _chunks(qs[i], i):
+                                await merged.put(chunk)
+                            finished[i] = True
+                            await merged.put(None)
+                        tasks = [asyncio.ensure_future(pump(i)) for i in range(n)]
+                        left = n
+                        while left:
+                            chunk = await merged.get()
+                            if chunk is None:
+                                left -= 1
+                            else:
+                                yield chunk
+                        await asyncio.gather(*tasks)
+                    yield _final()
+                finally:
+                    for i, q in enumerate(qs):
+                        if not finished[i]:   # client disconnected: free the request
+                            worker.cancel(q)
             return StreamingResponse(gen(), media_type="text/event-stream")
+        q = await _run(ids, params)
         res = await _collect(q, stops)
         out = res[0]
         choice = _choice(0, *res)

@@ -358,3 +358,27 @@ def test_logit_bias_field(client):
                                              "logit_bias": {"77": 100}}).json()
     assert r["choices"][0]["token_ids"] == [77, 77, 77]
     assert client.post("/v1/completions", json={"prompt": [5], "logit_bias": {"5": 1000}}).status_code == 400
+
+
+def test_stream_n_choices(client):
+    """n > 1 with stream: the choices' chunks interleave, each tagged with its
+    index, each choice finishes, one [DONE] (and one usage chunk) closes."""
+    with client.stream("POST", "/v1/completions", json={"prompt": [3, 4, 5], "max_tokens": 4, "temperature": 0.9,
+                                                        "seed": 11, "n": 3, "stream": True,
+                                                        "stream_options": {"include_usage": True}}) as s:
+        lines = [l for l in s.iter_lines() if l.startswith("data: ")]
+    assert lines[-1] == "data: [DONE]" and lines.count("data: [DONE]") == 1
+    evs = [json.loads(l[6:]) for l in lines[:-1]]
+    usage = evs[-1]
+    assert usage["choices"] == [] and usage["usage"]["completion_tokens"] == 12
+    toks = {0: [], 1: [], 2: []}
+    fins = {}
+    for e in evs[:-1]:
+        c = e["choices"][0]
+        toks[c["index"]].extend(c.get("token_ids") or [])
+        if c["finish_reason"]:
+            fins[c["index"]] = c["finish_reason"]
+    assert all(len(t) == 4 for t in toks.values()) and set(fins) == {0, 1, 2}
+    plain = client.post("/v1/completions", json={"prompt": [3, 4, 5], "max_tokens": 4, "temperature": 0.9,
+                                                 "seed": 11, "n": 3}).json()
+    assert [c["token_ids"] for c in plain["choices"]] == [toks[i] for i in range(3)]
