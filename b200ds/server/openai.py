@@ -795,6 +795,96 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
     async def models():
         return {"object": "list", "data": [{"id": model_name, "object": "model", "owned_by": "b200ds"}]}
 
+    # ---- SGLang-native endpoints (the reference's clients talk to SGLang) ----
+    def _sgl_params(sp: dict) -> SamplingParams:
+        body = {"max_tokens": sp.get("max_new_tokens", 128), "temperature": sp.get("temperature", 1.0),
+                "top_p": sp.get("top_p"), "top_k": sp.get("top_k") if (sp.get("top_k") or 0) > 0 else 0,
+                "seed": sp.get("sampling_seed", sp.get("seed")), "ignore_eos": sp.get("ignore_eos", False),
+                "stop_token_ids": sp.get("stop_token_ids"), "presence_penalty": sp.get("presence_penalty"),
+                "frequency_penalty": sp.get("frequency_penalty"),
+                "repetition_penalty": sp.get("repetition_penalty"), "min_p": sp.get("min_p"),
+                "min_tokens": sp.get("min_new_tokens"), "regex": sp.get("regex"),
+                "guided_json": (json.loads(sp["json_schema"]) if isinstance(sp.get("json_schema"), str)
+                                else sp.get("json_schema"))}
+        return _params({k: v for k, v in body.items() if v is not None}, default_max=128)
+
+    @app.post("/generate")
+    async def generate(request: Request):
+        """SGLang's /generate: {"text" | "input_ids" (one or a batch),
+        "sampling_params": {max_new_tokens, temperature, top_p, top_k, stop,
+        stop_token_ids, ignore_eos, penalties, min_new_tokens, regex,
+        json_schema}, "stream"} -> {"text", "output_ids", "meta_info"}."""
+        if not worker.healthy():
+            raise HTTPException(503, f"engine unavailable: {worker.health().get('error')}")
+        body = await request.json()
+        batch = body.get("input_ids") if body.get("input_ids") is not None else body.get("text")
+        single = not (isinstance(batch, list) and batch and isinstance(batch[0], (list, str)))
+        items = [batch] if single else batch
+        sp = body.get("sampling_params") or {}
+        try:
+            params = _sgl_params(sp)
+            prompts = [tok.encode(x) if isinstance(x, str) else list(x) for x in items]
+            for ids in prompts:
+                worker.engine.check_request(ids, params)
+        except (ValueError, TypeError) as e:
+            raise HTTPException(400, str(e))
+        stops = sp.get("stop") or []
+        stops = [stops] if isinstance(stops, str) else list(stops)
+
+        def meta(ids, out, reason):
+            fr = {"type": "stop"} if reason == "stop" else {"type": reason}
+            return {"prompt_tokens": len(ids), "completion_tokens": len(out), "finish_reason": fr}
+        if body.get("stream"):
+            if not single:
+                raise HTTPException(400, "stream takes one prompt")
+            q = await _run(prompts[0], params)
+
+            async def gen():
+                out, done = [], False
+                try:
+                    while True:
+                        ev = await q.get()
+                        if ev[0] == "error":
+                            yield f"data: {json.dumps({'error': {'message': ev[1]}})}\n\n"
+                            break
+                        if ev[0] == "tokens":
+                            out.extend(ev[1])
+                            text = tok.decode(out)
+                            cut, _ = _stop_scan(text, stops) if stops else (None, 0)
+                            if cut is not None:
+                                worker.cancel(q)
+                                yield f"data: {json.dumps({'text': text[:cut], 'output_ids': out, 'meta_info': meta(prompts[0], out, 'stop')})}\n\n"
+                                break
+                            yield f"data: {json.dumps({'text': text, 'output_ids': out, 'meta_info': meta(prompts[0], out, None)})}\n\n"
+                        else:
+                            yield f"data: {json.dumps({'text': tok.decode(out), 'output_ids': out, 'meta_info': meta(prompts[0], out, ev[1])})}\n\n"
+                            break
+                    done = True
+                    yield "data: [DONE]\n\n"
+                finally:
+                    if not done:
+                        worker.cancel(q)
+            return StreamingResponse(gen(), media_type="text/event-stream")
+        qs = [await _run(ids, params) for ids in prompts]
+        res = []
+        for ids, q in zip(prompts, qs):
+            out, text, reason, _, _ = await _collect(q, stops)
+            res.append({"text": text, "output_ids": out, "meta_info": meta(ids, out, reason)})
+        return res[0] if single else res
+
+    @app.get("/get_model_info")
+    async def get_model_info():
+        c = worker.engine.cfg
+        return {"model_path": model_name, "tokenizer_path": model_name, "is_generation": True,
+                "architecture": c.arch, "num_params": c.num_params()}
+
+    @app.get("/get_server_info")
+    async def get_server_info():
+        import dataclasses
+        e = worker.engine
+        return {"engine_config": dataclasses.asdict(e.ecfg), "model_config": e.cfg.to_dict(),
+                "tp_size": e.ps.tp_size, "ep_size": e.ps.ep_size, "dp_attention": bool(e.dp)}
+
     @app.post("/update_weights_from_disk")
     async def update_weights(request: Request):
         """{"model_path": checkpoint dir}: new weights of the same architecture,

@@ -382,3 +382,27 @@ def test_stream_n_choices(client):
     plain = client.post("/v1/completions", json={"prompt": [3, 4, 5], "max_tokens": 4, "temperature": 0.9,
                                                  "seed": 11, "n": 3}).json()
     assert [c["token_ids"] for c in plain["choices"]] == [toks[i] for i in range(3)]
+
+
+def test_sglang_native_endpoints(client):
+    """SGLang's /generate (single, batch, stream) and the info endpoints."""
+    r = client.post("/generate", json={"input_ids": [5, 6, 7], "sampling_params": {"max_new_tokens": 4,
+                                                                                  "temperature": 0}}).json()
+    assert len(r["output_ids"]) == 4 and r["meta_info"]["completion_tokens"] == 4
+    assert r["meta_info"]["finish_reason"]["type"] == "length"
+    same = client.post("/v1/completions", json={"prompt": [5, 6, 7], "max_tokens": 4, "temperature": 0}).json()
+    assert same["choices"][0]["token_ids"] == r["output_ids"]
+    b = client.post("/generate", json={"text": ["hi", "there"], "sampling_params": {"max_new_tokens": 2,
+                                                                                    "temperature": 0}}).json()
+    assert isinstance(b, list) and len(b) == 2 and all(len(x["output_ids"]) == 2 for x in b)
+    g = client.post("/generate", json={"text": "n:", "sampling_params": {"max_new_tokens": 6, "temperature": 0,
+                                                                         "regex": "[0-9]{3}"}}).json()
+    assert g["text"].isdigit() and len(g["text"]) == 3
+    with client.stream("POST", "/generate", json={"input_ids": [5, 6, 7], "stream": True,
+                                                  "sampling_params": {"max_new_tokens": 3, "temperature": 0}}) as s:
+        lines = [l for l in s.iter_lines() if l.startswith("data: ")]
+    assert lines[-1] == "data: [DONE]" and json.loads(lines[-2][6:])["output_ids"] == r["output_ids"][:3]
+    assert client.get("/get_model_info").json()["is_generation"]
+    info = client.get("/get_server_info").json()
+    assert info["engine_config"]["page_size"] == 8 and info["model_config"]["hidden_size"] == 256
+    assert client.post("/generate", json={"input_ids": [], "sampling_params": {}}).status_code == 400
