@@ -49,7 +49,7 @@ class EngineWorker:
             self.watchdog = Watchdog(watchdog_s, exit_code=70 if watchdog_exit else None)
         self.inbox: "queue.Queue" = queue.Queue()
         self.cancels: "queue.Queue" = queue.Queue()     # subscription queues whose client went away
-        self.commands: "queue.Queue" = queue.Queue()    # weight updates (path, loop, q)
+        self.commands: "queue.Queue" = queue.Queue()    # engine commands (kind, arg, loop, q): update / flush
         self.pending_update = None
         self.subs: Dict[int, tuple] = {}     # rid -> (loop, asyncio.Queue, emitted count)
         self._stop = threading.Event()
@@ -85,7 +85,11 @@ class EngineWorker:
     def request_update(self, path: str, loop, q) -> None:
         """Queue a weight update: admission pauses, the update runs on every
         rank once no request is in flight, the result is posted to q."""
-        self.commands.put((path, loop, q))
+        self.commands.put(("update", path, loop, q))
+
+    def request_flush(self, loop, q) -> None:
+        """Queue a prefix-cache flush (run like an update: idle, every rank)."""
+        self.commands.put(("flush", None, loop, q))
 
     def _update_due(self) -> bool:
         """Pick up a queued update; True when one is pending and nothing is in flight."""
@@ -96,10 +100,15 @@ class EngineWorker:
                 return False
         return not self.subs and not self.engine.sched.has_work
 
+    def _command_msg(self) -> dict:
+        kind, arg = self.pending_update[:2]
+        return {"new": [], "abort": [], kind: arg if kind == "update" else True}
+
     def _run_update(self) -> None:
-        path, loop, q = self.pending_update
+        msg = self._command_msg()
+        _, _, loop, q = self.pending_update
         self.pending_update = None
-        _post(loop, q, _apply_update(self.engine, path))
+        _post(loop, q, _apply_command(self.engine, msg))
 
     def _step(self):
         """One engine step under the watchdog (when configured)."""
@@ -161,7 +170,7 @@ class EngineWorker:
         while not self._stop.is_set():
             if self._update_due():
                 if self.ps is not None and self.ps.world_size > 1:
-                    _broadcast_requests(self.ps, {"new": [], "abort": [], "update": self.pending_update[0]})
+                    _broadcast_requests(self.ps, self._command_msg())
                 self._run_update()
                 continue
             new = []
@@ -206,10 +215,13 @@ class EngineWorker:
             _broadcast_requests(self.ps, None)      # followers stop
 
 
-def _apply_update(engine, path: str) -> tuple:
-    """engine.update_weights on this rank; ("updated", bytes) or ("error", why)."""
+def _apply_command(engine, msg: dict) -> tuple:
+    """An engine command on this rank: {"update": path} -> ("updated", bytes),
+    {"flush": True} -> ("flushed", pages); ("error", why) on failure."""
     try:
-        return ("updated", engine.update_weights(path))
+        if msg.get("update"):
+            return ("updated", engine.update_weights(msg["update"]))
+        return ("flushed", engine.flush_cache())
     except (ValueError, OSError, KeyError) as e:
         return ("error", f"{type(e).__name__}: {e}")
 
@@ -248,7 +260,7 @@ class DPEngineWorker(EngineWorker):
         world = ps.world_size
         while not self._stop.is_set():
             if self._update_due():
-                _broadcast_requests(ps, {"new": [], "abort": [], "update": self.pending_update[0]})
+                _broadcast_requests(ps, self._command_msg())
                 self._run_update()
                 continue
             new = self._admit() if self.pending_update is None else []
@@ -352,8 +364,8 @@ def dp_follower_loop(engine, ps) -> None:
         msg = _broadcast_requests(ps, None)
         if msg is None:
             return
-        if msg.get("update"):
-            _apply_update(engine, msg["update"])
+        if msg.get("update") or msg.get("flush"):
+            _apply_command(engine, msg)
             continue
         _dp_admit(engine, ps, msg["new"], own)
         _dp_abort(engine, msg["abort"], own)
@@ -371,8 +383,8 @@ def follower_loop(engine, ps) -> None:
         msg = _broadcast_requests(ps, None)
         if msg is None:
             return
-        if msg.get("update"):
-            _apply_update(engine, msg["update"])
+        if msg.get("update") or msg.get("flush"):
+            _apply_command(engine, msg)
             continue
         for prompt, spd in msg["new"]:
             r = engine.add_request(prompt, SamplingParams(**spd))
@@ -903,13 +915,15 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
 
     @app.post("/flush_cache")
     async def flush_cache():
-        """Clear the prefix cache when no request is in flight (409 otherwise)."""
-        if worker.subs or worker.engine.sched.has_work:
-            raise HTTPException(409, "requests are in flight")
-        try:
-            return {"success": True, "pages": worker.engine.flush_cache()}
-        except ValueError as e:
-            raise HTTPException(409, str(e))
+        """Clear the prefix cache (on the engine thread, once no request is in
+        flight, on every rank)."""
+        loop = asyncio.get_running_loop()
+        q: asyncio.Queue = asyncio.Queue()
+        worker.request_flush(loop, q)
+        kind, val = await q.get()
+        if kind == "error":
+            raise HTTPException(409, val)
+        return {"success": True, "pages": int(val)}
 
     @app.post("/tokenize")
     async def tokenize(request: Request):
