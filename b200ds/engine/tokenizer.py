@@ -3,6 +3,7 @@ tokenizer files is given, else a byte-level tokenizer (random-init models
 have no vocabulary; ids are bytes offset past the special tokens)."""
 from __future__ import annotations
 
+import json
 import os
 from typing import List, Optional
 
@@ -20,7 +21,7 @@ class ByteTokenizer:
     def encode(self, text: str) -> List[int]:
         return [b + 3 for b in text.encode("utf-8")]
 
-    def decode(self, ids: List[int]) -> str:
+    def decode(self, ids: List[int], keep_special: bool = False) -> str:
         return bytes([(i - 3) % 256 for i in ids if i >= 3]).decode("utf-8", errors="replace")
 
     def apply_chat_template(self, messages, add_generation_prompt: bool = True) -> str:
@@ -29,8 +30,9 @@ class ByteTokenizer:
             parts.append("<|assistant|>")
         return "".join(parts)
 
-    def encode_chat(self, messages) -> List[int]:
-        return self.encode(self.apply_chat_template(messages))
+    def encode_chat(self, messages, tools=None) -> List[int]:
+        head = f"<|tools|>{json.dumps(tools)}" if tools else ""
+        return self.encode(head + self.apply_chat_template(messages))
 
 
 class HFTokenizer:
@@ -42,16 +44,18 @@ class HFTokenizer:
     def encode(self, text: str) -> List[int]:
         return self.tok.encode(text, add_special_tokens=True)
 
-    def decode(self, ids: List[int]) -> str:
-        return self.tok.decode(ids, skip_special_tokens=True)
+    def decode(self, ids: List[int], keep_special: bool = False) -> str:
+        return self.tok.decode(ids, skip_special_tokens=not keep_special)
 
     def apply_chat_template(self, messages, add_generation_prompt: bool = True) -> str:
         return self.tok.apply_chat_template(messages, tokenize=False, add_generation_prompt=add_generation_prompt)
 
-    def encode_chat(self, messages) -> List[int]:
-        """Token ids of the chat template: the template writes its own BOS,
-        so the text is not encoded again with special tokens added."""
-        text = self.apply_chat_template(messages)
+    def encode_chat(self, messages, tools=None) -> List[int]:
+        """Token ids of the chat template (with the request's tools, when the
+        template renders them): the template writes its own BOS, so the text
+        is not encoded again with special tokens added."""
+        kw = {"tools": tools} if tools else {}
+        text = self.tok.apply_chat_template(messages, tokenize=False, add_generation_prompt=True, **kw)
         return self.tok.encode(text, add_special_tokens=False)
 
 

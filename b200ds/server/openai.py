@@ -592,7 +592,11 @@ def _params(body: dict, default_max: int = 16, chat: bool = False) -> SamplingPa
     )
 
 
-def create_app(worker: EngineWorker, model_name: str = "b200ds"):
+def create_app(worker: EngineWorker, model_name: str = "b200ds", reasoning: bool = False):
+    """The HTTP app.  reasoning: chat answers are split into
+    reasoning_content and content at "</think>" (DeepSeek-R1 style; not in
+    streamed deltas)."""
+    from .parsers import parse_tool_calls, split_reasoning
     from fastapi import FastAPI, HTTPException, Request
     from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
 
@@ -610,7 +614,7 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
             msgs = body.get("messages")
             if not isinstance(msgs, list):
                 raise HTTPException(400, "messages must be a list")
-            return tok.encode_chat(msgs)
+            return tok.encode_chat(msgs, body.get("tools"))
         p = body.get("prompt")
         if isinstance(p, list) and all(isinstance(i, int) for i in p):
             return p
@@ -677,11 +681,24 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds"):
 
         echo = bool(body.get("echo")) and not chat
 
+        tools = chat and bool(body.get("tools"))
+
         def _choice(i, out, text, reason, lps, plp=None):
             if echo:
                 text = tok.decode(ids) + text
-            c = ({"index": i, "message": {"role": "assistant", "content": text}, "finish_reason": reason} if chat
-                 else {"index": i, "text": text, "token_ids": out, "finish_reason": reason})
+            if chat:
+                msg = {"role": "assistant", "content": text}
+                if tools:                     # the tool-call markers are special tokens: decode them too
+                    msg["content"], calls = parse_tool_calls(tok.decode(out, keep_special=True))
+                    if calls:
+                        msg["tool_calls"] = calls
+                        msg["content"] = msg["content"] or None
+                        reason = "tool_calls"
+                if reasoning and isinstance(msg["content"], str):
+                    msg["reasoning_content"], msg["content"] = split_reasoning(msg["content"])
+                c = {"index": i, "message": msg, "finish_reason": reason}
+            else:
+                c = {"index": i, "text": text, "token_ids": out, "finish_reason": reason}
             if params.logprobs is not None:
                 c["logprobs"] = _lp_json(tok, lps, chat, prompt=(ids, plp) if echo else None)
             return c
@@ -986,6 +1003,8 @@ def main(argv=None):
     ap.add_argument("--watchdog-timeout", type=float, default=300.0,
                     help="seconds one engine step may run before /health reports a stall (0: off)")
     ap.add_argument("--watchdog-exit", action="store_true", help="exit the process when the watchdog fires")
+    ap.add_argument("--reasoning-parser", choices=("deepseek-r1",), default=None,
+                    help="split chat answers into reasoning_content and content")
     args = ap.parse_args(argv)
     import uvicorn
     from .. import load_engine
@@ -1012,7 +1031,8 @@ def main(argv=None):
         return
     wd = dict(watchdog_s=args.watchdog_timeout, watchdog_exit=args.watchdog_exit)
     worker = (DPEngineWorker(eng, tok, ps, **wd) if eng.dp else EngineWorker(eng, tok, ps, **wd)).start()
-    uvicorn.run(create_app(worker, model_name=str(args.model)), host=args.host, port=args.port, log_level="warning")
+    uvicorn.run(create_app(worker, model_name=str(args.model), reasoning=args.reasoning_parser is not None),
+                host=args.host, port=args.port, log_level="warning")
 
 
 if __name__ == "__main__":
