@@ -594,9 +594,9 @@ def _params(body: dict, default_max: int = 16, chat: bool = False) -> SamplingPa
 
 def create_app(worker: EngineWorker, model_name: str = "b200ds", reasoning: bool = False):
     """The HTTP app.  reasoning: chat answers are split into
-    reasoning_content and content at "</think>" (DeepSeek-R1 style; not in
-    streamed deltas)."""
-    from .parsers import parse_tool_calls, split_reasoning
+    reasoning_content and content at "</think>" (DeepSeek-R1 style; streamed
+    as reasoning_content / content deltas)."""
+    from .parsers import parse_tool_calls, split_reasoning, stream_reasoning
     from fastapi import FastAPI, HTTPException, Request
     from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
 
@@ -739,6 +739,7 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds", reasoning: bool
                 """Events of choice idx until it finishes."""
                 ids_all: List[int] = []
                 sent = 0                      # characters of the decoded text already streamed
+                r_sent = a_sent = 0           # reasoning / answer characters streamed (reasoning parser)
                 if echo:                      # the prompt's text first
                     yield _ev({"index": idx, "text": tok.decode(ids), "token_ids": [], "finish_reason": None})
                 while True:
@@ -758,7 +759,17 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds", reasoning: bool
                         end = cut if cut is not None else len(full) - hold
                         text = full[sent:end] if end > sent else ""
                         sent = max(sent, end)
-                        if text or cut is None:
+                        if chat and reasoning:      # deltas split into reasoning_content / content
+                            rs, ans = stream_reasoning(full[:end])
+                            delta = {}
+                            if len(rs) > r_sent:
+                                delta["reasoning_content"] = rs[r_sent:]
+                            if len(ans) > a_sent:
+                                delta["content"] = ans[a_sent:]
+                            r_sent, a_sent = max(r_sent, len(rs)), max(a_sent, len(ans))
+                            if delta:
+                                yield _ev({"index": idx, "delta": delta, "finish_reason": None})
+                        elif text or cut is None:
                             choice = ({"index": idx, "delta": {"content": text}, "finish_reason": None} if chat
                                       else {"index": idx, "text": text, "token_ids": val, "finish_reason": None})
                             if lp_field is not None:

@@ -60,3 +60,18 @@ def parse_tool_calls(text: str) -> Tuple[str, List[dict]]:
         calls.append({"id": "call_" + uuid.uuid4().hex[:24], "type": m.group("type"),
                       "function": {"name": m.group("name").strip(), "arguments": args}})
     return content, calls
+
+
+def stream_reasoning(text: str) -> Tuple[str, str]:
+    """(reasoning, answer) of a partial output for streaming: text that might
+    still become a "<think>" / "</think>" marker is held back."""
+    t = text
+    if THINK_OPEN.startswith(t.lstrip()) and len(t.lstrip()) < len(THINK_OPEN):
+        return "", ""                                       # maybe the opening marker
+    if t.lstrip().startswith(THINK_OPEN):
+        t = t.lstrip()[len(THINK_OPEN):]
+    i = t.find(THINK_CLOSE)
+    if i >= 0:
+        return t[:i], t[i + len(THINK_CLOSE):]
+    hold = next((k for k in range(min(len(THINK_CLOSE) - 1, len(t)), 0, -1) if THINK_CLOSE.startswith(t[-k:])), 0)
+    return t[: len(t) - hold], ""

@@ -36,6 +36,13 @@ def test_reasoning_content_over_http():
                                                  "temperature": 0, "guided_regex": "<think>[a-z]{3}</think>ok"})
         m = r.json()["choices"][0]["message"]
         assert len(m["reasoning_content"]) == 3 and m["content"] == "ok"
+        with c.stream("POST", "/v1/chat/completions", json={
+                "messages": [{"role": "user", "content": "q"}], "max_tokens": 40, "temperature": 0,
+                "guided_regex": "<think>[a-z]{3}</think>ok", "stream": True}) as st:
+            evs = [json.loads(l[6:]) for l in st.iter_lines() if l.startswith("data: ") and l != "data: [DONE]"]
+        deltas = [e["choices"][0]["delta"] for e in evs]
+        assert "".join(d.get("reasoning_content", "") for d in deltas) == m["reasoning_content"]
+        assert "".join(d.get("content", "") for d in deltas) == "ok"
         r = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "q"}], "max_tokens": 4,
                                                  "temperature": 0, "tools": [{"type": "function", "function": {
                                                      "name": "f", "parameters": {"type": "object"}}}]})
