@@ -207,7 +207,7 @@ def yarn_mscale(scale: float, mscale: float = 1.0) -> float:
 # ---------------------------------------------------------------------------
 
 def tiny_config(**over) -> ModelConfig:
-    """2 layers (dense FFN 512, then MoE), hidden 256,
+    """The tiny CPU / gloo plumbing model: 2 layers (dense FFN 512, then MoE), hidden 256,
     4 heads, q_lora 128, kv_lora 64, nope 32, rope 16, v 32, 8 experts top-2
     sigmoid + 1 shared, moe_intermediate 128, vocab 1024."""
     c = ModelConfig(
@@ -221,18 +221,18 @@ def tiny_config(**over) -> ModelConfig:
 
 
 def v3_671b_config(**over) -> ModelConfig:
-    """DeepSeek-V3 shaped 671B decoder."""
+    """The DeepSeek-V3-shaped 671B decoder (the headline benchmark model)."""
     return dataclasses.replace(ModelConfig(), **over)
 
 
 def v32_sparse_config(**over) -> ModelConfig:
-    """the 671B model with a 64-head fp8 lightning indexer
+    """The 671B model with a 64-head fp8 lightning indexer
     selecting top-2048 latent-KV tokens per query."""
     return dataclasses.replace(ModelConfig(index_n_heads=64, index_head_dim=128, index_topk=2048), **over)
 
 
 def v3_nvfp4_config(**over) -> ModelConfig:
-    """routed experts in NVFP4, shared/dense in MXFP8."""
+    """The 671B model with routed experts in NVFP4, shared/dense in MXFP8."""
     return dataclasses.replace(ModelConfig(expert_format="nvfp4", dense_format="mxfp8"), **over)
 
 

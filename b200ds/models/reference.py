@@ -7,7 +7,7 @@ V3.2 lightning indexer as an explicit score matrix + top-k.  It supports
 tensor parallelism (heads / FFN columns split, all-reduce after row-parallel
 projections; routed experts split across the same ranks with the shared
 expert column-split) through :class:`~b200ds.parallel.state.ParallelState`,
-so BASELINE config 1 (TP=2 over gloo) can be checked against a single process.
+so the tiny TP=2 gloo configuration can be checked against a single process.
 
 Reference parity: the served layer loop is fork_loop.py:229-400 (attention
 fork_attn.py:75-553, MoE moe_fwd.py:67-263); routing semantics follow the

@@ -31,7 +31,7 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-BASELINE_METRIC = "output tok/s/GPU on 8xB200 (device-timed, max over ranks); p50 TPOT, TTFT"
+HEADLINE_METRIC = "output tok/s/GPU on 8xB200 (device-timed, max over ranks); p50 TPOT, TTFT"
 
 
 class ClockSampler:
@@ -304,7 +304,7 @@ def main():
     clocks = sampler.summary()
     if ps.rank == 0:
         out = {
-            "metric": BASELINE_METRIC,
+            "metric": HEADLINE_METRIC,
             "value": round(value, 2),
             "unit": "output tokens/s (whole job)",
             "n_gpus": world,

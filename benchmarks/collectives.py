@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Fused-collective microbenchmark sweep (BASELINE config 5), one process per GPU:
+"""Fused-collective microbenchmark sweep, one process per GPU:
 
     torchrun --nproc-per-node N benchmarks/collectives.py
 

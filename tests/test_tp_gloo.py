@@ -1,4 +1,4 @@
-"""tiny DeepSeek-style model, fp32 on CPU, TP=2 over gloo.
+"""Tiny DeepSeek-style model, fp32 on CPU, TP=2 over gloo.
 Logits of a 2-rank run must match a single-process run to 1e-4."""
 import torch
 
