@@ -863,6 +863,9 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds", reasoning: bool
         sp = body.get("sampling_params") or {}
         try:
             params = _sgl_params(sp)
+            if body.get("return_logprob"):
+                import dataclasses
+                params = dataclasses.replace(params, logprobs=int(body.get("top_logprobs_num") or 0))
             prompts = [tok.encode(x) if isinstance(x, str) else list(x) for x in items]
             for ids in prompts:
                 worker.engine.check_request(ids, params)
@@ -871,9 +874,15 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds", reasoning: bool
         stops = sp.get("stop") or []
         stops = [stops] if isinstance(stops, str) else list(stops)
 
-        def meta(ids, out, reason):
+        def meta(ids, out, reason, lps=None):
             fr = {"type": "stop"} if reason == "stop" else {"type": reason}
-            return {"prompt_tokens": len(ids), "completion_tokens": len(out), "finish_reason": fr}
+            m = {"prompt_tokens": len(ids), "completion_tokens": len(out), "finish_reason": fr}
+            if lps is not None and params.logprobs is not None:
+                # SGLang's layout: [logprob, token id, text]
+                m["output_token_logprobs"] = [[lp, t, None] for t, lp, _ in lps]
+                if params.logprobs > 0:
+                    m["output_top_logprobs"] = [[[alp, a, None] for a, alp in top] for _, _, top in lps]
+            return m
         if body.get("stream"):
             if not single:
                 raise HTTPException(400, "stream takes one prompt")
@@ -908,8 +917,8 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds", reasoning: bool
         qs = [await _run(ids, params) for ids in prompts]
         res = []
         for ids, q in zip(prompts, qs):
-            out, text, reason, _, _ = await _collect(q, stops)
-            res.append({"text": text, "output_ids": out, "meta_info": meta(ids, out, reason)})
+            out, text, reason, lps, _ = await _collect(q, stops)
+            res.append({"text": text, "output_ids": out, "meta_info": meta(ids, out, reason, lps)})
         return res[0] if single else res
 
     @app.get("/get_model_info")

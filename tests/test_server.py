@@ -402,6 +402,10 @@ def test_sglang_native_endpoints(client):
                                                   "sampling_params": {"max_new_tokens": 3, "temperature": 0}}) as s:
         lines = [l for l in s.iter_lines() if l.startswith("data: ")]
     assert lines[-1] == "data: [DONE]" and json.loads(lines[-2][6:])["output_ids"] == r["output_ids"][:3]
+    lp = client.post("/generate", json={"input_ids": [5, 6, 7], "return_logprob": True, "top_logprobs_num": 2,
+                                        "sampling_params": {"max_new_tokens": 3, "temperature": 0}}).json()["meta_info"]
+    assert [x[1] for x in lp["output_token_logprobs"]] == r["output_ids"][:3]
+    assert all(x[0] <= 0 for x in lp["output_token_logprobs"]) and len(lp["output_top_logprobs"][0]) == 2
     assert client.get("/get_model_info").json()["is_generation"]
     info = client.get("/get_server_info").json()
     assert info["engine_config"]["page_size"] == 8 and info["model_config"]["hidden_size"] == 256
