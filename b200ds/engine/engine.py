@@ -50,6 +50,12 @@ class GenerateOutput:
     prompt_logprobs: Optional[List[Optional[tuple]]] = None   # per prompt token (None for the first)
 
 
+def _stop_hit(text: str, stops) -> Optional[int]:
+    """Index of the earliest stop string in text, or None."""
+    hits = [i for i in (text.find(st) for st in stops if st) if i >= 0]
+    return min(hits) if hits else None
+
+
 def _wants_plp(step) -> bool:
     """A prefill step with a request that asked for prompt log-probabilities."""
     return step.kind == "prefill" and any(r.params.prompt_logprobs is not None for r in step.reqs)
@@ -439,6 +445,8 @@ class Engine:
                     r.finished, r.finish_reason = True, "length"
                 elif not p.ignore_eos and ((self.eos is not None and t == self.eos) or t in p.stop_token_ids):
                     r.finished, r.finish_reason = True, "stop"
+                elif p.stop and self.tokenizer is not None and _stop_hit(self.tokenizer.decode(r.output), p.stop):
+                    r.finished, r.finish_reason = True, "stop"
                 if r.finished:
                     r.t_done = now
                     self.sched.finish(r)
@@ -780,6 +788,9 @@ class Engine:
         n = len(r.output)
         tpot = (r.t_done - r.t_first) / (n - 1) if n > 1 else 0.0
         text = self.tokenizer.decode(r.output) if self.tokenizer is not None else None
+        if text is not None and r.params.stop:
+            cut = _stop_hit(text, r.params.stop)
+            text = text if cut is None else text[:cut]
         return GenerateOutput(r.rid, len(r.prompt), list(r.output), r.finish_reason or "length",
                               (r.t_first or r.t_arrive) - r.t_arrive, tpot, text,
                               list(r.logprobs) if r.params.logprobs is not None else None,

@@ -17,6 +17,7 @@ class SamplingParams:
     seed: Optional[int] = None
     ignore_eos: bool = False
     stop_token_ids: List[int] = field(default_factory=list)
+    stop: List[str] = field(default_factory=list)    # stop strings (engine API; needs a tokenizer)
     logprobs: Optional[int] = None  # record each output token's log-probability and this many top alternatives
     presence_penalty: float = 0.0   # output tokens seen at least once lose this much logit
     frequency_penalty: float = 0.0  # ... and this much per occurrence

@@ -370,3 +370,15 @@ def test_priority_policy_admits_lower_priority_values_first():
         s.add(r)
     assert s.next_step().reqs == [b]
     assert [r.rid for r in s.waiting] == [1, 3]          # arrival order within a level
+
+
+def test_stop_strings_in_engine_api():
+    from b200ds.engine.tokenizer import ByteTokenizer
+    eng, cfg = _engine(False)
+    eng.tokenizer = ByteTokenizer()
+    p = eng.tokenizer.encode("go:")
+    full = eng.generate([p], SamplingParams(max_tokens=10))[0]
+    stop = full.text[3:5]
+    o = eng.generate([p], SamplingParams(max_tokens=10, stop=[stop]))[0]
+    assert o.finish_reason == "stop" and o.text == full.text[: full.text.find(stop)]
+    assert len(o.token_ids) < 10
