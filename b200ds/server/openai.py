@@ -26,6 +26,7 @@ Reference parity: the reference serves through SGLang's OpenAI server
 import argparse
 import asyncio
 import json
+import os
 import queue
 import threading
 import time
@@ -592,7 +593,8 @@ def _params(body: dict, default_max: int = 16, chat: bool = False) -> SamplingPa
     )
 
 
-def create_app(worker: EngineWorker, model_name: str = "b200ds", reasoning: bool = False):
+def create_app(worker: EngineWorker, model_name: str = "b200ds", reasoning: bool = False,
+               api_key: Optional[str] = None):
     """The HTTP app.  reasoning: chat answers are split into
     reasoning_content and content at "</think>" (DeepSeek-R1 style; streamed
     as reasoning_content / content deltas)."""
@@ -601,6 +603,19 @@ def create_app(worker: EngineWorker, model_name: str = "b200ds", reasoning: bool
     from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
 
     app = FastAPI(title="b200ds")
+
+    if api_key:
+        import hmac
+
+        @app.middleware("http")
+        async def _auth(request, call_next):
+            """Every endpoint but /health needs `Authorization: Bearer <api key>`."""
+            if request.url.path != "/health":
+                got = request.headers.get("authorization", "")
+                if not hmac.compare_digest(got.encode(), f"Bearer {api_key}".encode()):
+                    return JSONResponse({"error": {"message": "invalid API key", "type": "auth_error"}},
+                                        status_code=401)
+            return await call_next(request)
     tok = worker.tok
 
     async def _run(prompt_ids, params):
@@ -1023,6 +1038,8 @@ def main(argv=None):
     ap.add_argument("--watchdog-timeout", type=float, default=300.0,
                     help="seconds one engine step may run before /health reports a stall (0: off)")
     ap.add_argument("--watchdog-exit", action="store_true", help="exit the process when the watchdog fires")
+    ap.add_argument("--api-key", default=os.environ.get("B200_API_KEY"),
+                    help="require `Authorization: Bearer <key>` (also B200_API_KEY)")
     ap.add_argument("--reasoning-parser", choices=("deepseek-r1",), default=None,
                     help="split chat answers into reasoning_content and content")
     args = ap.parse_args(argv)
@@ -1051,7 +1068,8 @@ def main(argv=None):
         return
     wd = dict(watchdog_s=args.watchdog_timeout, watchdog_exit=args.watchdog_exit)
     worker = (DPEngineWorker(eng, tok, ps, **wd) if eng.dp else EngineWorker(eng, tok, ps, **wd)).start()
-    uvicorn.run(create_app(worker, model_name=str(args.model), reasoning=args.reasoning_parser is not None),
+    uvicorn.run(create_app(worker, model_name=str(args.model), reasoning=args.reasoning_parser is not None,
+                           api_key=args.api_key),
                 host=args.host, port=args.port, log_level="warning")
 
 

@@ -410,3 +410,19 @@ def test_sglang_native_endpoints(client):
     info = client.get("/get_server_info").json()
     assert info["engine_config"]["page_size"] == 8 and info["model_config"]["hidden_size"] == 256
     assert client.post("/generate", json={"input_ids": [], "sampling_params": {}}).status_code == 400
+
+
+def test_api_key():
+    from fastapi.testclient import TestClient
+    from b200ds import EngineConfig, load_engine
+    from b200ds.engine.tokenizer import ByteTokenizer
+    from b200ds.server.openai import EngineWorker, create_app
+    eng = load_engine("tiny", ecfg=EngineConfig(page_size=8, cuda_graphs=False), device="cpu")
+    worker = EngineWorker(eng, ByteTokenizer()).start()
+    with TestClient(create_app(worker, "tiny", api_key="s3cret")) as c:
+        body = {"prompt": [5, 6], "max_tokens": 2, "temperature": 0}
+        assert c.post("/v1/completions", json=body).status_code == 401
+        assert c.post("/v1/completions", json=body, headers={"Authorization": "Bearer nope"}).status_code == 401
+        ok = c.post("/v1/completions", json=body, headers={"Authorization": "Bearer s3cret"})
+        assert ok.status_code == 200 and c.get("/health").status_code == 200
+    worker.stop()
