@@ -56,6 +56,17 @@ def _stop_hit(text: str, stops) -> Optional[int]:
     return min(hits) if hits else None
 
 
+def _stop_in_tail(tok, output: List[int], stops) -> bool:
+    """Whether a stop string ends in the newest tokens of `output`.  Checked
+    after every token, so a stop string first completes in the output's tail:
+    only the last (longest stop string + 8) tokens are decoded (a token
+    decodes to at least one character, except special tokens and partial
+    UTF-8 bytes, which the margin covers), keeping the per-step cost
+    independent of the output length."""
+    w = max(len(st) for st in stops if st) + 8 if any(stops) else 0
+    return w > 0 and _stop_hit(tok.decode(output[-w:]), stops) is not None
+
+
 def _wants_plp(step) -> bool:
     """A prefill step with a request that asked for prompt log-probabilities."""
     return step.kind == "prefill" and any(r.params.prompt_logprobs is not None for r in step.reqs)
@@ -445,7 +456,7 @@ class Engine:
                     r.finished, r.finish_reason = True, "length"
                 elif not p.ignore_eos and ((self.eos is not None and t == self.eos) or t in p.stop_token_ids):
                     r.finished, r.finish_reason = True, "stop"
-                elif p.stop and self.tokenizer is not None and _stop_hit(self.tokenizer.decode(r.output), p.stop):
+                elif p.stop and self.tokenizer is not None and _stop_in_tail(self.tokenizer, r.output, p.stop):
                     r.finished, r.finish_reason = True, "stop"
                 if r.finished:
                     r.t_done = now

@@ -1,7 +1,10 @@
-"""Collectives used by the model.
+"""Eager collectives used by the model.
 
-``all_reduce`` runs the fused NVLink kernels when the symmetric workspace is
-set up (see b200ds.parallel.symm) and NCCL otherwise (the baseline path).
+``all_reduce`` is the plain NCCL all-reduce over the tensor-parallel group:
+the baseline path, and the eager path for prefill chunks larger than the
+fused kernels' symmetric slots.  The fused NVLink kernels (GEMM-epilogue
+push, combine + all-reduce + norm) are called from `b200ds.ops.cuda` through
+`b200ds.parallel.symm`, not from here.
 """
 from __future__ import annotations
 

@@ -123,6 +123,7 @@ def parse():
     p.add_argument("--model", default=None)
     p.add_argument("--batch", type=int, default=None)
     p.add_argument("--input-len", type=int, default=None)
+    p.add_argument("--output-len", type=int, default=None)
     p.add_argument("--weight-sets", type=int, default=0)
     p.add_argument("--trace", action="store_true",
                    help="device timestamps per layer phase inside the decode graph (adds launches: the step "
@@ -132,19 +133,21 @@ def parse():
     a.model = a.model or d["model"]
     a.batch = a.batch or d["batch"]
     a.input_len = a.input_len or d["input_len"]
+    a.output_len = a.output_len or d["output_len"]
     a.dp = bool(d.get("dp", False))
     return a
 
 
 # Named workloads (model preset, concurrent requests, input tokens each).
 BENCH_CONFIGS = {
-    "v3-1k": {"model": "deepseek-v3-671b", "batch": 64, "input_len": 1024},
-    "v32-sparse-32k": {"model": "deepseek-v3.2-sparse-671b", "batch": 8, "input_len": 32768},
-    # DP attention on every rank + EP over all ranks, 256 requests x 2K
-    "v3-dp-2k": {"model": "deepseek-v3-671b", "batch": 256, "input_len": 2048, "dp": True},
-    "v3-nvfp4-dp-2k": {"model": "deepseek-v3-671b-nvfp4", "batch": 256, "input_len": 2048, "dp": True},
+    "v3-1k": {"model": "deepseek-v3-671b", "batch": 64, "input_len": 1024, "output_len": 1024},
+    "v32-sparse-32k": {"model": "deepseek-v3.2-sparse-671b", "batch": 8, "input_len": 32768, "output_len": 1024},
+    # DP attention on every rank + EP over all ranks, 256 requests x 2K in, 512 out
+    "v3-dp-2k": {"model": "deepseek-v3-671b", "batch": 256, "input_len": 2048, "output_len": 512, "dp": True},
+    "v3-nvfp4-dp-2k": {"model": "deepseek-v3-671b-nvfp4", "batch": 256, "input_len": 2048, "output_len": 512,
+                       "dp": True},
     # the reference's served architecture: DeepSeek-V4.1-Flash shape (mHC, MQA + sinks, Engram, E5), NVFP4 experts
-    "v41-flash-1k": {"model": "deepseek-v4.1-flash", "batch": 64, "input_len": 1024},
+    "v41-flash-1k": {"model": "deepseek-v4.1-flash", "batch": 64, "input_len": 1024, "output_len": 1024},
 }
 
 
@@ -181,7 +184,9 @@ def main():
     if args.impl == "native":
         import b200ds._C  # noqa: F401
     cfg = PRESETS[args.model]()
-    ctx = args.input_len + args.warmup + 2 * args.steps + 8
+    # KV room for the whole output (1K in + 1K out reaches context 2K): decode is
+    # timed at contexts spread over the output (see context_points)
+    ctx = args.input_len + args.output_len + 2 * args.warmup + 2 * args.steps + 16
     # DP attention: each rank serves batch / world of the requests
     assert not args.dp or args.batch % world == 0, "DP attention needs batch % gpus == 0"
     local_batch = args.batch // world if args.dp else args.batch
@@ -252,22 +257,56 @@ def main():
         eng.step()
     barrier()
 
-    # ---- device-timed: back-to-back graph replays ---------------------------------
+    # ---- timed decode at contexts spread over the 1K output ----------------------
+    # The K timed steps are split over three context points (start of the
+    # output, its middle, its end), so the step time averages the attention
+    # cost over the whole output.  Each point: K_i back-to-back replays of the
+    # captured decode step (device-timed, max over ranks), then K_i steps
+    # through Engine.step (end to end).  Between points every running request
+    # is moved forward to the next context: its KV rows for the skipped
+    # positions are copies of its own earlier rows (the work per step depends
+    # on the context length only).
+    points = context_points(args.input_len, args.output_len, args.steps, args.warmup)
+    shares = [args.steps // len(points) + (1 if k < args.steps % len(points) else 0) for k in range(len(points))]
     gr = eng.graphs.graphs[eng.graphs._bucket(len(eng.sched.running))]
-    seqs = [{"tokens": [r.all_tokens[r.cached]], "start": r.cached, "pages": r.pages} for r in eng.sched.running]
-    eng.graphs.stage(gr, seqs)
-    barrier()
     sampler = ClockSampler(dev.index)
+    dev_ms, e2e_ms, step_times, per_point = 0.0, 0.0, [], []
     with sampler:
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        barrier()
-        e0.record()
-        for _ in range(args.steps):
-            gr.graph.replay()
-        e1.record()
-        barrier()
-    dev_ms = max_over_ranks(e0.elapsed_time(e1))
+        for ctx_target, k in zip(points, shares):
+            if k == 0:
+                continue
+            advance_context(eng, model, ctx_target, seed=ctx_target)
+            seqs = [{"tokens": [r.all_tokens[r.cached]], "start": r.cached, "pages": r.pages}
+                    for r in eng.sched.running]
+            eng.graphs.stage(gr, seqs)
+            barrier()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(k):
+                gr.graph.replay()
+            e1.record()
+            barrier()
+            d_ms = max_over_ranks(e0.elapsed_time(e1))
+            # end to end through the public API (host scheduling, pinned H2D of
+            # the step's inputs, replay, D2H of the sampled ids)
+            f0 = torch.cuda.Event(enable_timing=True)
+            f1 = torch.cuda.Event(enable_timing=True)
+            pt = []
+            f0.record()
+            for _ in range(k):
+                t = time.perf_counter()
+                eng.step()
+                pt.append(time.perf_counter() - t)
+            f1.record()
+            barrier()
+            f_ms = max_over_ranks(f0.elapsed_time(f1))
+            dev_ms += d_ms
+            e2e_ms += f_ms
+            step_times += pt
+            per_point.append({"context": ctx_target, "steps": k, "ms_per_step": round(d_ms / k, 3),
+                              "e2e_ms_per_step": round(f_ms / k, 3),
+                              "p50_tpot_ms": round(statistics.median(pt) * 1e3, 3)})
     step_ms = dev_ms / args.steps
     trace_us = None
     if args.trace and gr.trace_names:
@@ -277,28 +316,14 @@ def main():
         tr.names = gr.trace_names
         trace_us = {k: round(v, 1) for k, v in tr.summary(st).items()}
     value = args.batch * args.steps / (dev_ms / 1e3)
-
-    log(f"device-timed {step_ms:.2f} ms/step; e2e")
-    # ---- end to end through Engine.step --------------------------------------------
-    barrier()
-    step_times = []
-    f0 = torch.cuda.Event(enable_timing=True)
-    f1 = torch.cuda.Event(enable_timing=True)
-    f0.record()
-    for _ in range(args.steps):
-        t = time.perf_counter()
-        eng.step()
-        step_times.append(time.perf_counter() - t)
-    f1.record()
-    barrier()
-    e2e_ms = max_over_ranks(f0.elapsed_time(f1))
+    log(f"device-timed {step_ms:.2f} ms/step over contexts {points}")
     e2e_value = args.batch * args.steps / (e2e_ms / 1e3)
     tpot_p50 = statistics.median(step_times) * 1e3
 
     # token id, position, KV slot, length, block-table row, sampling params (4 x 4 B)
     h2d = local_batch * (4 + 4 + 8 + 4 + 16) + local_batch * eng.graphs.max_pages * 4
     d2h = local_batch * 8
-    launches = count_launches(gr) if args.impl == "native" else None
+    launches, graph_nodes = count_launches(gr) if args.impl == "native" else (None, None)
     if os.environ.get("B200_BENCH_PROFILE") == "1":
         profile_breakdown(gr, ps.rank)
     clocks = sampler.summary()
@@ -323,12 +348,17 @@ def main():
             "e2e": {"value": round(e2e_value, 2), "unit": "output tokens/s (whole job) via Engine.step",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,
+            # every kernel node of the decode graph (ours + torch / library glue)
+            "graph_kernel_nodes": graph_nodes,
             "clocks": clocks,
             "config": {"name": args.config, "model": args.model, "global_batch": args.batch,
-                       "seq_len": args.input_len,
-                       "context_during_timing": [args.input_len + args.warmup, args.input_len + args.warmup + 2 * args.steps],
+                       "seq_len": args.input_len, "output_len": args.output_len,
+                       "context_points": per_point,
                        "parallelism": (f"dp{world}-attn+ep{world}-moe" if args.dp else f"tp{world}-attn+ep{world}-moe"),
                        "expert_format": cfg.expert_format, "weight_sets": getattr(model, "weight_sets", None),
+                       "weight_format": "e4m3 weights with one UE8M0 scale per 32 K elements (MXFP8; the "
+                                        "checkpoint's 128x128 fp32 block scales are converted at load) and "
+                                        "activations quantized the same way per 32 (the config's 1x128)",
                        "switches": __import__("b200ds.utils.levers", fromlist=["switches"]).switches(),
                        "selfcheck": eng.selfcheck,
                        "l2": "no flush: per-step weights+KV >> 126 MB L2", "init_s": round(t_init, 1)},
@@ -337,22 +367,72 @@ def main():
             out["trace_us_per_step"] = trace_us      # traced run: timing includes the stamp launches
         print(json.dumps(out), flush=True)
     # Teardown: drop every reference to the captured graphs (they hold NCCL
-    # work) before the process group goes; a watchdog ends the process if the
-    # teardown stalls, since the result line is already out.
+    # work) before the process group goes.  The process then ends through the
+    # normal interpreter exit (exit handlers run); a daemon watchdog ends it
+    # only if the multi-rank teardown stalls, since the result line is out.
     gr = None
     eng.graphs.release()
     import gc
     gc.collect()
     torch.cuda.synchronize()
+    sys.stdout.flush()
+    sys.stderr.flush()
     if world > 1:
-        threading.Timer(30.0, lambda: os._exit(0)).start()
+        wd = threading.Timer(60.0, lambda: os._exit(0))
+        wd.daemon = True
+        wd.start()
         try:
             dist.destroy_process_group()
         except Exception as e:
             log(f"process-group teardown: {e}")
-    sys.stdout.flush()
-    sys.stderr.flush()
-    os._exit(0)
+        wd.cancel()
+
+
+def context_points(input_len: int, output_len: int, steps: int, warmup: int):
+    """Contexts at which decode is timed: the output's start (right after
+    prefill and warm-up), its middle and its end (input_len + output_len,
+    minus the room the timed steps need)."""
+    k = steps // 3 + 1
+    first = input_len + warmup
+    last = input_len + output_len - 2 * k - 1
+    mid = (first + last) // 2
+    return [first, mid, last] if last > mid > first else [first]
+
+
+def advance_context(eng, model, target: int, seed: int = 0) -> None:
+    """Move every running request forward to `target` cached tokens without
+    running the model: output tokens are appended (uniform-random ids), pages
+    allocated, and the KV rows (every per-slot cache tensor of the model) of
+    the new positions copied from the request's own rows at position
+    (p mod cached-so-far).  Decode work per step depends on the context
+    length only, so this reaches a later context at no compute cost."""
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    ps = eng.ecfg.page_size
+    src, dst = [], []
+    for r in eng.sched.running:
+        have = r.cached
+        if target <= have:
+            continue
+        n_new = target - have
+        r.output.extend(torch.randint(0, eng.cfg.vocab_size, (n_new,), generator=g).tolist())
+        if not eng.sched._ensure_pages(r, target + 1):
+            raise RuntimeError("KV pool too small for the timed contexts")
+        for p in range(have, target):
+            q = p % have
+            dst.append(r.pages[p // ps] * ps + p % ps)
+            src.append(r.pages[q // ps] * ps + q % ps)
+        r.cached = target
+    if not dst:
+        return
+    dev = model.device
+    si = torch.tensor(src, dtype=torch.int64, device=dev)
+    di = torch.tensor(dst, dtype=torch.int64, device=dev)
+    for t in model.kv_tensors():
+        if t.dim() >= 1 and t.shape[0] >= int(max(max(src), max(dst))) + 1:
+            t.index_copy_(0, di, t.index_select(0, si))
+    if dev.type == "cuda":
+        torch.cuda.synchronize()
 
 
 def profile_breakdown(gr, rank: int) -> None:
@@ -374,12 +454,13 @@ def profile_breakdown(gr, rank: int) -> None:
               f"n={e.count:4d} {e.key[:100]}", file=sys.stderr)
 
 
-def count_launches(gr) -> int:
-    """Kernels of the b200ds extension in one replay of the decode graph,
-    read from the captured graph's kernel nodes (no profiler)."""
+def count_launches(gr):
+    """(kernels of the b200ds extension, all kernel nodes) in one replay of
+    the decode graph, read from the captured graph's kernel nodes (no
+    profiler)."""
     from b200ds import _C
     total, ours = _C.graph_kernel_count(gr.graph.raw_cuda_graph())
-    return int(ours)
+    return int(ours), int(total)
 
 
 if __name__ == "__main__":

@@ -426,6 +426,11 @@ def main():
         ("gemm_o_proj_T64", lambda: run_gemm("o_proj", 64, 7168, 16384, a.iters)),
         ("gemm_o_proj_tp8_T64", lambda: run_gemm("o_proj_tp8", 64, 7168, 2048, a.iters)),
         ("add_rmsnorm_quant_T64", lambda: run_norm(64, a.iters)),
+        # prefill shapes (compute-bound)
+        ("gemm_dense_T4096", lambda: run_gemm("dense_T4096", 1024 if small else 4096, 7168, 7168, a.iters)),
+        ("gemm_o_proj_T512", lambda: run_gemm("o_proj_T512", 512, 7168, 2048, a.iters)),
+        ("moe_mxfp8_T2048_ep1", lambda: run_moe("mxfp8", 512 if small else 2048, 256, 64 if small else 256,
+                                                 a.iters)),
         ("v4_T64", lambda: run_v4(64, a.iters)),
     ]
     for name, fn in cases:

@@ -59,7 +59,11 @@ int b200_mla_tc(const MlaTcArgs* args, cudaStream_t st);
 // [T,H,512].  Returns 0 or a B200_NOALLOC_ERR_* code (see
 // b200_mla_decode_noalloc_error).  Calls share the scratch, so calls that
 // overlap on the GPU race; the first call on a device sets up the scratch
-// addresses and should come before any stream capture.
+// addresses and should come before any stream capture.  The stream must
+// belong to the current device (a stream of another device is rejected as
+// a bad argument).  Kernel-side failures (a bounded wait that ran out of
+// time) set a sticky status word in the library: b200_mla_decode_noalloc_status
+// waits for the stream, returns the word (0 = fine) and clears it.
 // This entry point has no counterpart in the reference.
 // ---------------------------------------------------------------------------
 #define B200_NOALLOC_ERR_BAD_ARG (-1)
@@ -71,3 +75,4 @@ extern "C" int b200_mla_decode_noalloc(const void* q_abs, const void* q_pe, int 
                                        const int* q_pos, int page_size, float sm_scale, float kv_scale, int nsplit,
                                        void* out, cudaStream_t stream);
 extern "C" const char* b200_mla_decode_noalloc_error(int code);
+extern "C" int b200_mla_decode_noalloc_status(cudaStream_t stream, unsigned int* status);

@@ -658,7 +658,14 @@ int b200_mla_tc(const MlaTcArgs* a, cudaStream_t st) {
 // Nothing in the scratch needs to start at zero: each call writes every
 // element it later reads.  The first call on a device looks up the arrays'
 // device addresses (cudaGetSymbolAddress) with that device current; make
-// that first call before any stream capture.
+// that first call before any stream capture.  The stream passed must belong
+// to the current device (checked: a stream of another device is rejected).
+//
+// Errors inside the kernels (a bounded mbarrier wait that ran out of time)
+// set bits in a status word that also lives in the library (sticky across
+// calls, zero at load).  b200_mla_decode_noalloc_status reads it after the
+// stream's work and clears it, so a caller can tell a timed-out decode from
+// a good one without allocating anything.
 // ===========================================================================
 #include <mutex>
 
@@ -669,6 +676,7 @@ static __device__ __align__(256) uint8_t g_noalloc_q8[kNoAllocMaxRows * 576];
 static __device__ __align__(256) float g_noalloc_qscale[kNoAllocMaxRows];
 static __device__ __align__(256) float g_noalloc_part_o[kNoAllocMaxPartRows * 512];
 static __device__ __align__(256) float g_noalloc_part_lse[kNoAllocMaxPartRows];
+static __device__ __align__(256) uint32_t g_noalloc_err;   // kernel status bits (sticky until read)
 
 constexpr int kMaxDevices = 64;
 struct NoAllocScratch {
@@ -677,6 +685,7 @@ struct NoAllocScratch {
   float* qscale = nullptr;
   float* part_o = nullptr;
   float* part_lse = nullptr;
+  uint32_t* err = nullptr;
 };
 NoAllocScratch g_scratch[kMaxDevices];
 std::mutex g_scratch_mu;
@@ -689,6 +698,7 @@ int noalloc_setup(int dev) {
   if (cudaGetSymbolAddress(reinterpret_cast<void**>(&s.qscale), g_noalloc_qscale) != cudaSuccess) return -1;
   if (cudaGetSymbolAddress(reinterpret_cast<void**>(&s.part_o), g_noalloc_part_o) != cudaSuccess) return -1;
   if (cudaGetSymbolAddress(reinterpret_cast<void**>(&s.part_lse), g_noalloc_part_lse) != cudaSuccess) return -1;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&s.err), g_noalloc_err) != cudaSuccess) return -1;
   s.ready = true;
   return 0;
 }
@@ -705,6 +715,10 @@ extern "C" __attribute__((visibility("default"))) int b200_mla_decode_noalloc(
     return B200_NOALLOC_ERR_TOO_LARGE;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return B200_NOALLOC_ERR_SETUP;
+  if (stream != nullptr) {                 // the scratch addresses are the current device's
+    int sdev = -1;
+    if (cudaStreamGetDevice(stream, &sdev) != cudaSuccess || sdev != dev) return B200_NOALLOC_ERR_BAD_ARG;
+  }
   if (noalloc_setup(dev) != 0) return B200_NOALLOC_ERR_SETUP;
   const NoAllocScratch& s = g_scratch[dev];
   if (b200_mla_q_quant(q_abs, q_pe, T * H, s.q8, s.qscale, stream) != 0) return B200_NOALLOC_ERR_LAUNCH;
@@ -726,14 +740,32 @@ extern "C" __attribute__((visibility("default"))) int b200_mla_decode_noalloc(
   a.out = out;
   a.part_o = s.part_o;
   a.part_lse = s.part_lse;
+  a.err = s.err;
   return b200_mla_tc(&a, stream) == 0 ? 0 : B200_NOALLOC_ERR_LAUNCH;
+}
+
+// Waits for `stream`, copies the kernels' status word of the current device
+// into *status (0 = every call since the last read finished its waits) and
+// clears it.  No allocation: one copy to the caller's host word, one memset.
+extern "C" __attribute__((visibility("default"))) int b200_mla_decode_noalloc_status(cudaStream_t stream,
+                                                                                    unsigned int* status) {
+  if (!status) return B200_NOALLOC_ERR_BAD_ARG;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return B200_NOALLOC_ERR_SETUP;
+  if (noalloc_setup(dev) != 0) return B200_NOALLOC_ERR_SETUP;
+  uint32_t* e = g_scratch[dev].err;
+  if (cudaMemcpyAsync(status, e, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
+      cudaMemsetAsync(e, 0, sizeof(uint32_t), stream) != cudaSuccess || cudaStreamSynchronize(stream) != cudaSuccess)
+    return B200_NOALLOC_ERR_LAUNCH;
+  return 0;
 }
 
 extern "C" __attribute__((visibility("default"))) const char* b200_mla_decode_noalloc_error(int code) {
   switch (code) {
     case 0: return "ok";
     case B200_NOALLOC_ERR_BAD_ARG:
-      return "bad argument (null pointer, T/H <= 0, H not a multiple of 16, nsplit outside 1..16, page size != 64)";
+      return "bad argument (null pointer, T/H <= 0, H not a multiple of 16, nsplit outside 1..16, page size != 64, "
+             "or a stream of another device than the current one)";
     case B200_NOALLOC_ERR_TOO_LARGE:
       return "request exceeds the static scratch: need T*H <= 4096 and nsplit*T*H <= 4096";
     case B200_NOALLOC_ERR_SETUP: return "could not look up the scratch arrays' device addresses";
