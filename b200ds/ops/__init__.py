@@ -288,6 +288,11 @@ def mla_attention(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size, to
                                        rope_table=rope_table)
     if rope_table is not None:
         q_pe = ref.rope(q_pe, fb.positions, rope_table)
+    if _use_baseline(q_abs) and topk is None and cache.dtype == torch.float8_e4m3fn:
+        from . import baseline
+        if fb.is_decode and page_size in (32, 64) and baseline.flashinfer_ok():
+            return baseline.mla_decode_flashinfer(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size)
+        return baseline.mla_prefill_torch(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size)
     out = ref.mla_attention(q_abs, q_pe, cache, kv_scale, fb.block_table, fb.seq_lens, fb.q_seq,
                             fb.positions, softmax_scale, page_size, topk)
     return out.to(q_abs.dtype) if q_abs.is_cuda else out
@@ -368,6 +373,10 @@ def moe_experts(h, w: torch.Tensor, ids: torch.Tensor, ex: ExpertWeights, out_dt
         if _IMPL == "native":
             return _native().moe_experts(h, w, ids, ex, out_dtype, n_experts_total, combine)
         from . import baseline
+        if baseline.flashinfer_ok() and n_experts_total is not None:
+            xb = h.hf if isinstance(h, QAct) and h.hf is not None else (
+                dequant_mxfp8(h.q, h.sf).to(torch.bfloat16) if isinstance(h, QAct) else h.to(torch.bfloat16))
+            return baseline.moe_experts_flashinfer(xb.contiguous(), w, ids, ex, n_experts_total).to(out_dtype)
         return baseline.moe_experts(h if isinstance(h, QAct) else quant(h), w, ids, ex, out_dtype)
     xf = to_float(h)
     T = xf.shape[0]

@@ -7,6 +7,14 @@ local partial into every rank's slot (P2P stores over NVLink) and then runs
 the reduce + residual + RMSNorm + MXFP8 kernel; steps with more tokens than
 `max_tokens` (long prefill chunks) use NCCL instead.
 
+NVLS mode (`nvls` switch, groups of at least `B200_NVLS_MIN_WORLD` ranks whose
+GPUs support multicast): a second symmetric buffer is bound to an NVLink
+multicast object.  Producers store their partial only into their own input
+slot; the reduction kernel sums each rank's share of the rows in the switch
+(multimem.ld_reduce), broadcasts it (multimem.st) and runs the same
+residual + RMSNorm + quant epilogue.  Per rank, one read and one write of
+1/world of the rows cross NVLink instead of world - 1 full copies.
+
 Reference parity: symmetric-memory rendezvous of the EPA / LGP buffers
 (epa.py:994-1010, lgp.py:272-291).
 """
@@ -25,6 +33,7 @@ class FusedAllReduce:
         self.hidden = hidden
         self.max_tokens = max_tokens
         self.push_ctas = push_ctas
+        is_tp = group != "ep"
         if group == "ep":       # expert-parallel reduce-scatter under DP attention
             self.world, self.rank, group = ps.ep_size, ps.ep_rank, ps.ep_group
         else:
@@ -42,11 +51,24 @@ class FusedAllReduce:
         self.ticket = torch.zeros(1, dtype=torch.int32, device=dev)        # reduce-side ticket
         self.push_ticket = torch.zeros(1, dtype=torch.int32, device=dev)   # push-side ticket
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        # NVLS only for the tensor-parallel all-reduce (the expert-parallel
+        # reduce-scatter keeps the push protocol)
+        self.nvls = (_Nvls.create(ps, name, group, self.world, self.rank, max_tokens, hidden, dev)
+                     if self.world > 1 and is_tp else None)
         torch.cuda.synchronize(dev)
         dist.barrier(group=group)
 
     def supports(self, T: int) -> bool:
         return 0 < T <= self.max_tokens
+
+    def _push_target(self):
+        """(bases, epoch, push ticket, multicast address) the producers of an
+        all-reduce write to: the NVLS buffer's own slot, or every rank's
+        push slot."""
+        n = self.nvls
+        if n is not None:
+            return n.bases, n.epoch, n.push_ticket, n.mc
+        return self.bases, self.epoch, self.push_ticket, 0
 
     def allreduce_add_rmsnorm(self, a: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float,
                               quantize: bool, keep_bf16: bool = True):
@@ -55,15 +77,11 @@ class FusedAllReduce:
         from ..ops.cuda import alloc_qact
         T, H = a.shape
         x = a if (a.dtype == torch.bfloat16 and a.is_contiguous()) else a.to(torch.bfloat16).contiguous()
-        _C.ar_push(x, self.bases, self.rank, self.max_tokens, self.epoch, self.push_ticket, self.push_ctas)
+        bases, epoch, ticket, mc = self._push_target()
+        _C.ar_push(x, bases, self.rank, self.max_tokens, epoch, ticket, self.push_ctas, mc=mc)
         y = torch.empty(T, H, dtype=torch.bfloat16, device=a.device) if (keep_bf16 or not quantize) else None
         qa = alloc_qact(T, H, a.device) if quantize else None
-        _C.ar_reduce_norm(T, H, self.bases, self.rank, self.max_tokens, self.epoch, self.ticket, 1,
-                          residual, w, eps, y, qa.q if qa else None, qa.sf if qa else None, self.err)
-        if qa is not None:
-            qa.hf = y
-            return qa, residual
-        return y, residual
+        return self._reduce(T, H, 1, residual, w, eps, y, qa)
 
     def _outs(self, T, H, dev, quantize, keep_bf16=True):
         from ..ops.cuda import alloc_qact
@@ -71,10 +89,15 @@ class FusedAllReduce:
         qa = alloc_qact(T, H, dev) if quantize else None
         return y, qa
 
-    def _reduce(self, T, H, push_ctas, residual, w, eps, y, qa):
+    def _reduce(self, T, H, push_ctas, residual, w, eps, y, qa, nvls: bool = True):
         from .. import _C
-        _C.ar_reduce_norm(T, H, self.bases, self.rank, self.max_tokens, self.epoch, self.ticket, push_ctas,
-                          residual, w, eps, y, qa.q if qa else None, qa.sf if qa else None, self.err)
+        n = self.nvls if nvls else None
+        if n is not None:
+            _C.nvls_ar_norm(T, H, n.bases, self.rank, self.max_tokens, n.mc, n.epoch, n.ticket, push_ctas,
+                            residual, w, eps, y, qa.q if qa else None, qa.sf if qa else None, self.err)
+        else:
+            _C.ar_reduce_norm(T, H, self.bases, self.rank, self.max_tokens, self.epoch, self.ticket, push_ctas,
+                              residual, w, eps, y, qa.q if qa else None, qa.sf if qa else None, self.err)
         if qa is not None:
             qa.hf = y
             return qa, residual
@@ -93,8 +116,9 @@ class FusedAllReduce:
         if splits < 2 or T > 128:
             from ..ops.cuda import gemm
             return self.allreduce_add_rmsnorm(gemm(a, wq), residual, ln_w, eps, quantize)
-        n = _C.gemm_push(wq.data, wq.sf, a.q, a.sf, N, T, K, splits, self.bases, self.rank, self.max_tokens,
-                         self.epoch, self.push_ticket)
+        bases, epoch, ticket, mc = self._push_target()
+        n = _C.gemm_push(wq.data, wq.sf, a.q, a.sf, N, T, K, splits, bases, self.rank, self.max_tokens,
+                         epoch, ticket, mc=mc)
         y, qa = self._outs(T, N, a.q.device, quantize)
         return self._reduce(T, N, int(n), residual, ln_w, eps, y, qa)
 
@@ -105,8 +129,9 @@ class FusedAllReduce:
         T = part.pair_row.shape[0]
         H = part.y.shape[1]
         add = part.add.to(torch.bfloat16).contiguous() if part.add is not None else None
-        _C.moe_combine_push(part.y, part.pair_row, add, self.bases, self.rank, self.max_tokens, self.epoch,
-                            self.push_ticket, self.push_ctas)
+        bases, epoch, ticket, mc = self._push_target()
+        _C.moe_combine_push(part.y, part.pair_row, add, bases, self.rank, self.max_tokens, epoch, ticket,
+                            self.push_ctas, mc=mc)
         y, qa = self._outs(T, H, part.y.device, quantize)
         return self._reduce(T, H, 1, residual, ln_w, eps, y, qa)
 
@@ -120,13 +145,57 @@ class FusedAllReduce:
         _C.ep_combine_rs(part.y, part.pair_row, part.T_step, part.T_r, add, self.bases, self.rank, self.max_tokens,
                          self.epoch, self.push_ticket, self.push_ctas)
         y, qa = self._outs(part.T_r, H, part.y.device, quantize)
-        return self._reduce(part.T_r, H, 1, residual, ln_w, eps, y, qa)
+        return self._reduce(part.T_r, H, 1, residual, ln_w, eps, y, qa, nvls=False)
 
     def check(self) -> None:
         """Raise if a bounded wait inside the kernels timed out."""
         e = int(self.err.item())
         if e:
             raise RuntimeError(f"fused all-reduce: peer wait timed out (code {e})")
+
+
+class _Nvls:
+    """The multicast-bound all-reduce buffer of one group (see the module
+    docstring): symmetric allocation, its multicast address, and the device
+    epoch / tickets of the NVLS protocol (csrc/comm/allreduce.cu)."""
+
+    @staticmethod
+    def create(ps, name, group, world, rank, max_tokens, hidden, dev):
+        """An _Nvls when the `nvls` switch is on, the group is large enough
+        and every rank got a multicast mapping (agreed with MIN over the CPU
+        group, so all ranks take the same path); else None."""
+        import os
+        from ..utils import levers
+        want = levers.on("nvls") and world >= int(os.environ.get("B200_NVLS_MIN_WORLD", "4"))
+        if not want:
+            return None
+        obj, ok = None, 0
+        try:
+            obj = _Nvls(name, world, rank, max_tokens, hidden, dev)
+            ok = 1 if obj.mc else 0
+        except Exception as e:   # no multicast on this box: the push protocol stays
+            levers.announce("nvls-off", f"NVLS all-reduce unavailable ({type(e).__name__}: {e})")
+        if not levers.agree_min([ok], getattr(ps, "cpu_group", None))[0]:
+            return None
+        levers.announce("nvls-on", f"NVLS all-reduce on ({world} ranks)")
+        return obj
+
+    def __init__(self, name, world, rank, max_tokens, hidden, dev):
+        import torch.distributed._symmetric_memory as symm_mem
+        from .. import _C
+        if not symm_mem._SymmetricMemory.has_multicast_support(symm_mem.DeviceType.CUDA, torch.device(dev).index):
+            raise RuntimeError("the device has no multicast support")
+        nbytes = int(_C.nvls_buffer_size(max_tokens, hidden))
+        self.buf = symm_mem.empty(nbytes, dtype=torch.uint8, device=dev)
+        self.buf.zero_()
+        self.hdl = symm_mem.rendezvous(self.buf, name)
+        if int(getattr(self.hdl, "offset", 0) or 0) != 0:
+            raise RuntimeError("symmetric buffer at a nonzero offset of its allocation")
+        self.mc = int(self.hdl.multicast_ptr or 0)
+        self.bases = [int(p) for p in self.hdl.buffer_ptrs]
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.ticket = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.push_ticket = torch.zeros(1, dtype=torch.int32, device=dev)
 
 
 class EPDispatch:

@@ -120,6 +120,9 @@ register("moe_pull", "B200_MOE_PULL", True,
          "fused experts read FC1 rows in place (activations / EP dispatch buffer) instead of a sorted copy")
 register("fused_comm", "B200_FUSED_COMM", True,
          "device-initiated NVLink collectives fused into the producing / consuming kernels")
+register("nvls", "B200_NVLS", True,
+         "tensor-parallel all-reduces through NVLink multicast (multimem.ld_reduce / multimem.st in the switch) on "
+         "groups of B200_NVLS_MIN_WORLD (default 4) or more ranks with multicast support")
 register("deterministic", "B200_DETERMINISTIC", False,
          "bitwise-reproducible steps: split-K GEMMs that sum with fp32 atomics (router logits, mHC stats) run "
          "unsplit")

@@ -430,7 +430,8 @@ def advance_context(eng, model, target: int, seed: int = 0) -> None:
     di = torch.tensor(dst, dtype=torch.int64, device=dev)
     for t in model.kv_tensors():
         if t.dim() >= 1 and t.shape[0] >= int(max(max(src), max(dst))) + 1:
-            t.index_copy_(0, di, t.index_select(0, si))
+            v = t.view(torch.uint8) if t.element_size() == 1 else t    # no fp8 index kernels
+            v.index_copy_(0, di, v.index_select(0, si))
     if dev.type == "cuda":
         torch.cuda.synchronize()
 

@@ -343,13 +343,17 @@ TUNE_GEMMS = [  # DeepSeek-V3 671B decode GEMMs (N, K) at TP1 and TP8 widths
 TUNE_ROWS = (1, 8, 16, 32, 64, 128)
 
 
-def tune(path: str, iters: int) -> None:
+def tune(path: str, iters: int, quick: bool = False) -> None:
+    """quick: one GEMM shape at two row counts and one MLA shape (a smoke run
+    of the whole procedure)."""
     from b200ds.ops import QAct, cuda, tactics
     dev = torch.device("cuda")
     table = {"gemm_splits": [], "mla_splits": []}
-    for name, N, K in TUNE_GEMMS:
+    gemms = TUNE_GEMMS[:1] if quick else TUNE_GEMMS
+    rows = (8, 64) if quick else TUNE_ROWS
+    for name, N, K in gemms:
         w = _mx((), N, K, dev)
-        for T in TUNE_ROWS:
+        for T in rows:
             x = cuda.quant(torch.randn(T, K, device=dev).to(torch.bfloat16))
             tactics.set_table({})
             default = cuda.choose_splits(T, N, K)
@@ -363,8 +367,8 @@ def tune(path: str, iters: int) -> None:
             table["gemm_splits"].append({"N": N, "K": K, "rows": T, "value": best})
             print(json.dumps({"tune": f"gemm_{name}", "T": T, "default": default, "best": best,
                               "us": {str(k): round(v * 1e6, 2) for k, v in times.items()}}), flush=True)
-    for H in (16, 128):
-        for B in (8, 64):
+    for H in ((16,) if quick else (16, 128)):
+        for B in ((8,) if quick else (8, 64)):
             times = {}
             for s in (1, 2, 3, 4, 6, 8):
                 tactics.set_table({"mla_splits": [{"H": H, "rows": B, "keys": [0, 2048], "value": s}]})
@@ -384,13 +388,14 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--small", action="store_true", help="reduced sizes (ncu captures)")
     ap.add_argument("--tune", default="", help="measure the legal tactics and write this tactics table (JSON)")
+    ap.add_argument("--tune-quick", action="store_true", help="with --tune: a reduced set of shapes")
     a = ap.parse_args()
     import b200ds._C  # noqa: F401
     from b200ds import ops
     ops.set_impl("native")
     torch.cuda.set_device(0)
     if a.tune:
-        tune(a.tune, a.iters)
+        tune(a.tune, a.iters, quick=a.tune_quick)
         return
     small = a.small
     cases = [

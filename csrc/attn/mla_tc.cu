@@ -5,10 +5,14 @@
 // 128B swizzle + one 64-byte rope box with 64B swizzle):
 //
 //   MMA1  S^T[128 tok, HB] = K[128 tok, 576] . Q[HB, 576]^T      (kind::f8f6f4)
-//   softmax warpgroup: S^T -> registers -> smem transpose; per-head running
-//         max in the log2 domain, raised only when a tile exceeds it by more
-//         than 8 (so P = 2^(x - m) <= 256 fits e4m3 and O rarely needs a
-//         rescale); P written as e4m3 into the MMA2 B operand (MN-major)
+//   softmax warps: S^T -> registers (thread = token row x half of the
+//         heads); head-wise tile max by a butterfly over the warp plus one
+//         shared-memory exchange between the four warps of a column half;
+//         per-head running max in the log2 domain, raised only when a tile
+//         exceeds it by more than 8 (so P = 2^(x - m) <= 256 fits e4m3 and O
+//         rarely needs a rescale); P written from registers as e4m3 into the
+//         MMA2 B operand (MN-major); the softmax denominators accumulate per
+//         thread and are reduced once, in the epilogue
 //   MMA2  O^T[512, HB] += V^T[512, 128 tok] . P^T[128 tok, HB]    (4 x M=128)
 //
 // KV tokens are the MMA's M (128) dimension and heads the N dimension, so a
@@ -19,7 +23,8 @@
 // Warp roles (320 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA
 // issuer, warps 2-9 softmax / correction / epilogue (two warps per TMEM
 // subpartition, each owning half of the head columns: the per-tile softmax
-// is the kernel's critical path).  All waits bounded.
+// is the kernel's critical path, one named barrier per tile).  All waits
+// bounded.
 //
 // Sparse variant (SPARSE = true): the query attends only to the cache
 // positions in its top-k list (-1 = unused entry).  The KV rows of a tile are
@@ -58,19 +63,18 @@ struct Smem {
   static constexpr int kKVRope = kTile * 64;            // 8 KB
   static constexpr int kKVStage = kKVLat + kKVRope;     // 72 KB
   static constexpr int kP = kTile * HB;                 // e4m3 P^T
-  static constexpr int kS = kTile * (HB + 1) * 4;       // fp32 transpose (padded)
   static constexpr int kOffQ = 0;
   static constexpr int kOffKV = ((kQLat + kQRope + 1023) / 1024) * 1024;
   static constexpr int kOffP = kOffKV + kStages * kKVStage;
   static constexpr int kPPad = ((kP + 127) / 128) * 128;
   // P^T double-buffered (softmax of tile i overlaps MMA2 of tile i - 1) when
   // it fits next to two KV stages; 64-head groups keep one buffer.
-  static constexpr int kPB = (kOffP + 2 * kPPad + kTile * (HB + 1) * 4 + 2 * kSmThreads * 4 + 8 * HB * 4 + 256 + 1024
-                              <= 227 * 1024) ? 2 : 1;
+  static constexpr int kRed = 2 * 2 * 4 * (HB / 2) * 4;  // [parity][half][warp][HB/2] fp32 partial maxima
+  static constexpr int kPB = (kOffP + 2 * kPPad + kRed + 256 + 1024 <= 227 * 1024) ? 2 : 1;
   static constexpr int kOffS = kOffP + kPB * kPPad;
-  static constexpr int kOffRed = kOffS + kS;            // 2 x kSmThreads floats
-  static constexpr int kOffHead = kOffRed + 2 * kSmThreads * 4;  // per-head state
-  static constexpr int kOffBar = kOffHead + 8 * HB * 4;
+  static constexpr int kOffRed = kOffS;
+  static constexpr int kOffHead = kOffRed + kRed;
+  static constexpr int kOffBar = kOffHead;
   static constexpr int kBytes = kOffBar + 256 + 1024;
   static_assert(kBytes <= 227 * 1024, "shared memory");
   static constexpr int kTmemS = 0;                      // 2 x HB columns
@@ -103,6 +107,32 @@ struct Params {
 
 __device__ __forceinline__ void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 
+// Column reduction of N values per lane over the warp's 32 lanes (max, or
+// sum when MX is false) in N - 1 + 5 - log2(N) shuffles: at each step the
+// lanes split the remaining columns in two halves, keep one and send the
+// other to their partner; afterwards lane l holds column l >> (5 - log2 N)
+// in v[0].  Compile-time sizes keep every index static (registers only).
+template <int N, int OFF, bool MX>
+__device__ __forceinline__ void col_reduce(float* v, int lane) {
+  if constexpr (OFF >= 1) {
+    if constexpr (N > 1) {
+      const bool upper = (lane & OFF) != 0;
+#pragma unroll
+      for (int j = 0; j < N / 2; ++j) {
+        const float give = upper ? v[j] : v[j + N / 2];
+        const float keep = upper ? v[j + N / 2] : v[j];
+        const float got = __shfl_xor_sync(0xffffffffu, give, OFF);
+        v[j] = MX ? fmaxf(keep, got) : keep + got;
+      }
+      col_reduce<N / 2, OFF / 2, MX>(v, lane);
+    } else {
+      const float got = __shfl_xor_sync(0xffffffffu, v[0], OFF);
+      v[0] = MX ? fmaxf(v[0], got) : v[0] + got;
+      col_reduce<1, OFF / 2, MX>(v, lane);
+    }
+  }
+}
+
 template <int HB, bool SPARSE>
 __global__ void __launch_bounds__(kThreads, 1)
 mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constant__ CUtensorMap tm_q_rope,
@@ -114,10 +144,7 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
   uint8_t* sQ = sm + S::kOffQ;
   uint8_t* sKV = sm + S::kOffKV;
   uint8_t* sP = sm + S::kOffP;
-  float* sS = reinterpret_cast<float*>(sm + S::kOffS);
   float* sRed = reinterpret_cast<float*>(sm + S::kOffRed);
-  float* sHead = reinterpret_cast<float*>(sm + S::kOffHead);   // [0:HB) factor, [HB:2HB) m, [2HB:3HB) l, [3HB:4HB) alpha
-  int* sFlag = reinterpret_cast<int*>(sHead + 4 * HB);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kOffBar);
   uint64_t* kv_full = bars;              // [2]
   uint64_t* kv_empty = bars + 2;         // [2]
@@ -151,11 +178,11 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
       mbar_init(&kv_full[i], SPARSE ? 32 : 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 1);
+      mbar_init(&s_free[i], kSmThreads / 32);    // one arrival per softmax warp
     }
     mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&p_full[i], 1);
+      mbar_init(&p_full[i], kSmThreads / 32);    // one arrival per softmax warp
       mbar_init(&o_done[i], 1);
     }
     fence_barrier_init();
@@ -280,102 +307,127 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
     if (ok && nt > 0) mma2(nt - 1);
   } else {
     // ---------------------- softmax / correction / epilogue ----------------------
-    const int tid = threadIdx.x - 64;            // 0..255
+    // Thread = one token row of the tile (TMEM lane) x NC = HB/2 head columns
+    // held in registers: warps 2-5 take heads [0, NC), warps 6-9 [NC, HB).
+    // Per tile: the head-wise tile max is reduced in registers (butterfly over
+    // the warp) and across the four warps of a column half through shared
+    // memory (the tile's only named barrier); P is written straight from
+    // registers into the MMA2 operand; the softmax denominator accumulates
+    // per thread (its rows) and is reduced once at the end.
+    constexpr int NC = HB / 2;
+    constexpr int kLogNC = NC == 8 ? 3 : NC == 16 ? 4 : 5;
     const int sub = warp & 3;                    // TMEM subpartition
-    const int hc0 = ((warp - 2) >> 2) * (HB / 2);   // this warp's half of the head columns
+    const int half = (warp - 2) >> 2;            // column half
+    const int hc0 = half * NC;
     const int row = sub * 32 + lane;             // token row of S^T / latent row of O^T
-    constexpr int QN = kSmThreads / HB;          // threads per head in the reduction
-    const int hh = tid % HB, part = tid / HB;
-    if (tid < HB) {
-      sHead[tid] = p.q_scale[(int64_t)t * p.H + h0 + tid] * p.qk_factor;
-      sHead[HB + tid] = -INFINITY;
-      sHead[2 * HB + tid] = 0.f;
+    const int wslot = (warp - 2) & 3;            // this warp's slot among the 4 of its half
+    const int mycol = lane >> (5 - kLogNC);      // column whose max / sum this lane holds after a reduction
+    float fac[NC], m[NC], lrow[NC];
+#pragma unroll
+    for (int j = 0; j < NC; ++j) {
+      fac[j] = p.q_scale[(int64_t)t * p.H + h0 + hc0 + j] * p.qk_factor;
+      m[j] = -INFINITY;
+      lrow[j] = 0.f;
     }
-    if (tid == 0) sFlag[0] = 0;
-    named_bar(1, kSmThreads);
+    // sRed: [2 tile parities][2 halves][4 warps][NC] partial maxima.
+    // A wait that runs out of time clears `ok`; the warp then skips its
+    // remaining waits but keeps taking part in every named barrier, so the
+    // eight warps never disagree on the barrier count.
     bool ok = true;
     for (int i = 0; i < nt; ++i) {
-      if (!mbar_wait(&s_full[i & 1], (i >> 1) & 1, p.err)) { ok = false; break; }
+      if (ok && !mbar_wait(&s_full[i & 1], (i >> 1) & 1, p.err)) ok = false;
       tc_fence_after();
       const int tok0 = k_lo + i * kTile;
-      // 1. S^T row -> scaled log2 scores in the padded transpose buffer
+      float x[NC];
       {
-        const uint32_t base = tmem + S::kTmemS + (i & 1) * HB + (uint32_t(sub * 32) << 16);
+        const uint32_t base = tmem + S::kTmemS + (i & 1) * HB + hc0 + (uint32_t(sub * 32) << 16);
 #pragma unroll
-        for (int c0 = hc0; c0 < hc0 + HB / 2; c0 += 8) {
+        for (int c0 = 0; c0 < NC; c0 += 8) {
           uint32_t r[8];
           tmem_ld_x8(base + c0, r);
           tmem_ld_wait();
-          bool valid = tok0 + row < k_hi;
-          if (SPARSE && valid) {
-            const int pos = __ldcg(p.topk + (int64_t)t * p.topk_n + tok0 + row);
-            valid = pos >= 0 && pos < n;
-          }
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            sS[row * (HB + 1) + c0 + j] = valid ? __uint_as_float(r[j]) * sHead[c0 + j] : -INFINITY;
+          for (int j = 0; j < 8; ++j) x[c0 + j] = __uint_as_float(r[j]);
         }
       }
       tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[i & 1]);      // this warp's S^T columns are read
+      bool valid = tok0 + row < k_hi;
+      if (SPARSE && valid) {
+        const int pos = __ldcg(p.topk + (int64_t)t * p.topk_n + tok0 + row);
+        valid = pos >= 0 && pos < n;
+      }
+      float v[NC];
+#pragma unroll
+      for (int j = 0; j < NC; ++j) {
+        x[j] = valid ? x[j] * fac[j] : -INFINITY;
+        v[j] = x[j];
+      }
+      // butterfly max over the warp's 32 rows: lane ends with column `mycol`
+      col_reduce<NC, 16, true>(v, lane);
+      float* red = sRed + ((i & 1) * 2 + half) * 4 * NC;
+      if ((lane & ((32 >> kLogNC) - 1)) == 0) red[wslot * NC + mycol] = v[0];
       named_bar(1, kSmThreads);
-      if (tid == 0) mbar_arrive(&s_free[i & 1]);
-      // 2. per-head tile max
-      float mx = -INFINITY;
-      for (int j = part; j < kTile; j += QN) mx = fmaxf(mx, sS[j * (HB + 1) + hh]);
-      sRed[part * HB + hh] = mx;
-      named_bar(1, kSmThreads);
-      if (tid < HB) {
-        float m = -INFINITY;
-        for (int q = 0; q < QN; ++q) m = fmaxf(m, sRed[q * HB + tid]);
-        const float mold = sHead[HB + tid];
-        float alpha = 1.f;
-        if (m > mold + kRescaleThresh || mold == -INFINITY) {
-          const float mnew = m;
-          alpha = (mold == -INFINITY) ? 0.f : exp2f(mold - mnew);
-          sHead[HB + tid] = mnew;
-          if (mold != -INFINITY) sFlag[0] = 1;
+      // new running max (raised lazily: only when a tile exceeds it by more
+      // than kRescaleThresh, so P = 2^(x - m) <= 256 fits e4m3)
+      bool changed = false;
+      float alpha[NC];
+#pragma unroll
+      for (int j = 0; j < NC; ++j) {
+        const float mt = fmaxf(fmaxf(red[j], red[NC + j]), fmaxf(red[2 * NC + j], red[3 * NC + j]));
+        alpha[j] = 1.f;
+        if (mt > m[j] + kRescaleThresh || (m[j] == -INFINITY && mt != -INFINITY)) {
+          alpha[j] = (m[j] == -INFINITY) ? 0.f : exp2f(m[j] - mt);
+          if (m[j] != -INFINITY) changed = true;
+          m[j] = mt;
         }
-        sHead[3 * HB + tid] = alpha;
       }
-      named_bar(1, kSmThreads);
-      // 3. P = 2^(x - m) -> e4m3 (<= 256); partial sums of the quantized P
-      const float m = sHead[HB + hh];
-      float lsum = 0.f;
       // P^T buffer (i % kPB) was last read by MMA2 of tile i - kPB
-      if (i >= S::kPB && !mbar_wait(&o_done[(i - S::kPB) & 1], ((i - S::kPB) >> 1) & 1, p.err)) { ok = false; }
+      if (ok && i >= S::kPB && !mbar_wait(&o_done[(i - S::kPB) & 1], ((i - S::kPB) >> 1) & 1, p.err)) ok = false;
       uint8_t* sPi = sP + (i % S::kPB) * S::kPPad;
-      for (int j = part; j < kTile; j += QN) {
-        const float x = sS[j * (HB + 1) + hh];
-        const float pv = (x == -INFINITY) ? 0.f : exp2f(x - m);
-        const uint16_t q2 = f2_to_e4m3x2(pv, 0.f);
-        const uint8_t qb = uint8_t(q2 & 0xFF);
-        __nv_fp8_e4m3 f8;
-        f8.__x = qb;
-        lsum += float(f8);
-        // MN-major no-swizzle core-matrix layout: [k group j/8][n chunk h/16][8 x 16]
-        sPi[(j >> 3) * (HB / 16) * 128 + (hh >> 4) * 128 + (j & 7) * 16 + (hh & 15)] = qb;
+      // P = 2^(x - m) as e4m3 into the MN-major core-matrix layout
+      // [k group row/8][n chunk h/16][8 x 16]; the row sum uses the quantized P
+#pragma unroll
+      for (int c0 = 0; c0 < NC; c0 += 16) {
+        constexpr int W16 = NC < 16 ? NC : 16;
+        uint32_t pk[W16 / 4];
+#pragma unroll
+        for (int j = 0; j < W16; j += 2) {
+          const int a = c0 + j;
+          const float p0 = (x[a] == -INFINITY) ? 0.f : exp2f(x[a] - m[a]);
+          const float p1 = (x[a + 1] == -INFINITY) ? 0.f : exp2f(x[a + 1] - m[a + 1]);
+          const uint16_t q2 = f2_to_e4m3x2(p0, p1);
+          __nv_fp8_e4m3 f0, f1;
+          f0.__x = uint8_t(q2 & 0xFF);
+          f1.__x = uint8_t(q2 >> 8);
+          lrow[a] = lrow[a] * alpha[a] + float(f0);
+          lrow[a + 1] = lrow[a + 1] * alpha[a + 1] + float(f1);
+          if ((j & 2) == 0) pk[j >> 2] = q2;
+          else pk[j >> 2] |= uint32_t(q2) << 16;
+        }
+        const int h = hc0 + c0;
+        uint8_t* dstp = sPi + (row >> 3) * (HB / 16) * 128 + (h >> 4) * 128 + (row & 7) * 16 + (h & 15);
+        if constexpr (W16 == 16) {
+          *reinterpret_cast<uint4*>(dstp) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        } else {
+          *reinterpret_cast<uint2*>(dstp) = make_uint2(pk[0], pk[1]);
+        }
       }
-      sRed[kSmThreads + part * HB + hh] = lsum;
-      named_bar(1, kSmThreads);
-      if (tid < HB) {
-        float l = 0.f;
-        for (int q = 0; q < QN; ++q) l += sRed[kSmThreads + q * HB + tid];
-        sHead[2 * HB + tid] = sHead[2 * HB + tid] * sHead[3 * HB + tid] + l;
-      }
-      // 4. rescale O^T columns whose max moved (rare): after MMA2 of tile i - 1
-      if (sFlag[0] && i >= 1) {
+      // rescale this warp's O^T columns whose max moved (rare): after MMA2 of tile i - 1
+      if (__any_sync(0xffffffffu, changed) && i >= 1 && ok) {
         if (!mbar_wait(&o_done[(i - 1) & 1], ((i - 1) >> 1) & 1, p.err)) ok = false;
         tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
-          const uint32_t ob = tmem + S::kTmemO + c * HB + (uint32_t(sub * 32) << 16);
+          const uint32_t ob = tmem + S::kTmemO + c * HB + hc0 + (uint32_t(sub * 32) << 16);
 #pragma unroll
-          for (int c0 = hc0; c0 < hc0 + HB / 2; c0 += 8) {
+          for (int c0 = 0; c0 < NC; c0 += 8) {
             uint32_t r[8];
             tmem_ld_x8(ob + c0, r);
             tmem_ld_wait();
 #pragma unroll
-            for (int j = 0; j < 8; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * sHead[3 * HB + c0 + j]);
+            for (int j = 0; j < 8; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * alpha[c0 + j]);
             tmem_st_x8(ob + c0, r);
           }
         }
@@ -383,30 +435,40 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      named_bar(1, kSmThreads);
-      if (tid == 0) {
-        sFlag[0] = 0;
-        mbar_arrive(&p_full[i & 1]);
-      }
-      if (!ok) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[i & 1]);      // this warp's P rows (and O^T rescale) are done
     }
-    // 5. epilogue: O^T (lane = latent row within block c, column = head)
+    // softmax denominators: sum of lrow over the 128 rows, per head
+    float l[NC];
+    {
+      float v[NC];
+#pragma unroll
+      for (int j = 0; j < NC; ++j) v[j] = lrow[j];
+      col_reduce<NC, 16, false>(v, lane);
+      named_bar(1, kSmThreads);                        // every warp is past its last tile's max exchange
+      float* red = sRed + half * 4 * NC;
+      if ((lane & ((32 >> kLogNC) - 1)) == 0) red[wslot * NC + mycol] = v[0];
+      named_bar(1, kSmThreads);
+#pragma unroll
+      for (int j = 0; j < NC; ++j) l[j] = (red[j] + red[NC + j]) + (red[2 * NC + j] + red[3 * NC + j]);
+    }
+    // epilogue: O^T (lane = latent row within block c, column = head)
     if (nt > 0 && ok && mbar_wait(&o_done[(nt - 1) & 1], ((nt - 1) >> 1) & 1, p.err)) {
       tc_fence_after();
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
-        const uint32_t ob = tmem + S::kTmemO + c * HB + (uint32_t(sub * 32) << 16);
+        const uint32_t ob = tmem + S::kTmemO + c * HB + hc0 + (uint32_t(sub * 32) << 16);
         const int d = c * 128 + row;
 #pragma unroll
-        for (int c0 = hc0; c0 < hc0 + HB / 2; c0 += 8) {
+        for (int c0 = 0; c0 < NC; c0 += 8) {
           uint32_t r[8];
           tmem_ld_x8(ob + c0, r);
           tmem_ld_wait();
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const int h = c0 + j;
-            const float l = sHead[2 * HB + h];
-            const float o = l > 0.f ? __uint_as_float(r[j]) * p.kv_scale / l : 0.f;
+            const int h = hc0 + c0 + j;
+            const float lj = l[c0 + j];
+            const float o = lj > 0.f ? __uint_as_float(r[j]) * p.kv_scale / lj : 0.f;
             const int64_t oi = ((int64_t)t * p.H + h0 + h) * kL + d;
             if (p.nsplit == 1) {
               p.out[oi] = __float2bfloat16(o);
@@ -416,17 +478,24 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
           }
         }
       }
-      if (tid < HB && (p.nsplit > 1 || p.lse_out)) {
-        const float l = sHead[2 * HB + tid];
-        const float v = l > 0.f ? sHead[HB + tid] + log2f(l) : -INFINITY;
-        if (p.nsplit > 1) p.part_lse[(int64_t)split * gridDim.x * p.H + (int64_t)t * p.H + h0 + tid] = v;
-        else p.lse_out[(int64_t)t * p.H + h0 + tid] = v;
+      if (sub == 0 && lane < NC && (p.nsplit > 1 || p.lse_out)) {
+        // lane j of warp (sub 0) of each half writes head hc0 + j
+        float lj = 0.f, mj = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < NC; ++j)
+          if (j == lane) { lj = l[j]; mj = m[j]; }
+        const float v = lj > 0.f ? mj + log2f(lj) : -INFINITY;
+        const int h = hc0 + lane;
+        if (p.nsplit > 1) p.part_lse[(int64_t)split * gridDim.x * p.H + (int64_t)t * p.H + h0 + h] = v;
+        else p.lse_out[(int64_t)t * p.H + h0 + h] = v;
       }
-    } else if (tid < HB && (p.nsplit > 1 || p.lse_out)) {
+    } else if (sub == 0 && lane < NC && (p.nsplit > 1 || p.lse_out)) {
       // empty split
-      if (p.nsplit > 1) p.part_lse[(int64_t)split * gridDim.x * p.H + (int64_t)t * p.H + h0 + tid] = -INFINITY;
-      else p.lse_out[(int64_t)t * p.H + h0 + tid] = -INFINITY;
+      const int h = hc0 + lane;
+      if (p.nsplit > 1) p.part_lse[(int64_t)split * gridDim.x * p.H + (int64_t)t * p.H + h0 + h] = -INFINITY;
+      else p.lse_out[(int64_t)t * p.H + h0 + h] = -INFINITY;
     }
+    const int tid = threadIdx.x - 64;
     if (nt == 0 && p.nsplit == 1) {
       for (int e = tid; e < HB * kL; e += kSmThreads)
         p.out[((int64_t)t * p.H + h0) * kL + e] = __float2bfloat16(0.f);

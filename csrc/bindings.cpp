@@ -156,7 +156,7 @@ void gemm(const at::Tensor& w, const at::Tensor& w_sf, int64_t w_sf_estride, con
 // Returns the number of CTAs that publish (the reduce kernel's expected count).
 int64_t gemm_push(const at::Tensor& w, const at::Tensor& w_sf, const at::Tensor& x, const at::Tensor& x_sf,
                   int64_t nw, int64_t t, int64_t k, int64_t splits, std::vector<int64_t> bases, int64_t rank,
-                  int64_t max_t, const at::Tensor& epoch, at::Tensor ticket) {
+                  int64_t max_t, const at::Tensor& epoch, at::Tensor ticket, int64_t mc) {
   check_cuda(w, "w");
   const c10::cuda::CUDAGuard g(w.device());
   TORCH_CHECK(k % 128 == 0 && nw % 128 == 0, "k, nw multiples of 128");
@@ -166,6 +166,7 @@ int64_t gemm_push(const at::Tensor& w, const at::Tensor& w_sf, const at::Tensor&
   pe.rank = rank;
   pe.world = bases.size();
   pe.max_t = max_t;
+  pe.mc = reinterpret_cast<uint8_t*>(mc);
   GemmArgs a{};
   a.w = ptr<uint8_t>(w);
   a.w_sf = ptr<uint8_t>(w_sf);
@@ -441,7 +442,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("q8"), pybind11::arg("qs"), pybind11::arg("q"), pybind11::arg("sf"),
         pybind11::arg("splits") = 1);
   m.def("gemm", &gemm);
-  m.def("gemm_push", &gemm_push);
+  m.def("gemm_push", &gemm_push, pybind11::arg("w"), pybind11::arg("w_sf"), pybind11::arg("x"), pybind11::arg("x_sf"),
+        pybind11::arg("nw"), pybind11::arg("t"), pybind11::arg("k"), pybind11::arg("splits"), pybind11::arg("bases"),
+        pybind11::arg("rank"), pybind11::arg("max_t"), pybind11::arg("epoch"), pybind11::arg("ticket"),
+        pybind11::arg("mc") = 0);
   m.def("rope", &rope);
   m.def("kv_store", &kv_store);
   m.def("router", &router, pybind11::arg("logits"), pybind11::arg("bias"), pybind11::arg("G"),

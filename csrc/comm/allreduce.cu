@@ -46,53 +46,15 @@ __device__ __forceinline__ void publish_push(const ArPeers& peers, int parity, u
 }
 
 
-// ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(kThreads) ar_push_kernel(const __nv_bfloat16* __restrict__ x, int T, int hidden,
-                                                           ArPeers peers, const uint32_t* epoch, uint32_t* ticket) {
-  pdl_wait();
-  if (threadIdx.x == 0) pdl_launch_dependents();   // e.g. the next GEMM prefetches weights during our wait
-  const int p = (*epoch) & 1;
-  const int64_t n16 = (int64_t)T * hidden / 8;       // 16-byte vectors
-  const int64_t per = (n16 + gridDim.x - 1) / gridDim.x;
-  const int64_t v0 = blockIdx.x * per;
-  const int64_t v1 = min(n16, v0 + per);
-  const uint4* src = reinterpret_cast<const uint4*>(x);
-  for (int q = 0; q < peers.world; ++q) {
-    uint4* dst = reinterpret_cast<uint4*>(recv_slot(peers.base[q], p, peers.rank, peers.world, peers.max_t, hidden));
-    for (int64_t v = v0 + threadIdx.x; v < v1; v += blockDim.x) dst[v] = src[v];
-  }
-  publish_push(peers, p, ticket);
-}
-
-// ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(kThreads) ar_reduce_norm_kernel(
-    int T, int hidden, ArPeers peers, uint32_t* epoch, uint32_t* ticket, uint32_t expected, float* residual,
-    const float* __restrict__ w, float eps, __nv_bfloat16* y, uint8_t* q, uint8_t* sf, uint32_t* err) {
-  __shared__ float red[32];
-  __shared__ int ok_s;
-  pdl_wait();
-  if (threadIdx.x == 0) pdl_launch_dependents();   // e.g. the next GEMM prefetches weights during our wait
-  const int p = (*epoch) & 1;
-  uint8_t* mine = peers.base[peers.rank];
-  if (threadIdx.x == 0) {
-    int ok = 1;
-    const uint32_t* cnt = counters(mine, p);
-    const uint64_t t0 = globaltimer_ns();
-    for (int src = 0; src < peers.world && ok; ++src) {
-      while (ld_acquire_sys(cnt + src) < expected) {
-        if (globaltimer_ns() - t0 > kWaitBudgetNs) {
-          atomicExch(err, kErrPeerTimeout);
-          ok = 0;
-          break;
-        }
-      }
-    }
-    ok_s = ok;
-  }
-  __syncthreads();
-  const int row = blockIdx.x;
+// Row epilogue shared by the push and NVLS reductions: v = sum of the nsrc
+// bf16 rows (src0 + i * src_stride, in index order) + residual (updated in
+// place, fp32); RMSNorm; bf16 y and / or MXFP8 q + sf (tcgen05 scale layout).
+// One CTA of kThreads per row; `red` is >= 32 floats of shared memory.
+__device__ __forceinline__ void row_add_norm_quant(int row, int hidden, const __nv_bfloat16* src0, int64_t src_stride,
+                                                   int nsrc, float* residual, const float* __restrict__ w, float eps,
+                                                   __nv_bfloat16* y, uint8_t* q, uint8_t* sf, float* red) {
   const int units = hidden >> 3;
-  if (ok_s && row < T) {
+  {
     float v[kMaxIt][8];
     float ss = 0.f;
 #pragma unroll
@@ -101,8 +63,8 @@ __global__ void __launch_bounds__(kThreads) ar_reduce_norm_kernel(
       if (u < units) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[it][i] = 0.f;
-        for (int src = 0; src < peers.world; ++src) {
-          const __nv_bfloat16* s = recv_slot(mine, p, src, peers.world, peers.max_t, hidden) + (int64_t)row * hidden;
+        for (int src = 0; src < nsrc; ++src) {
+          const __nv_bfloat16* s = src0 + src * src_stride + (int64_t)row * hidden;
           const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(s + u * 8));
           const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
@@ -179,6 +141,55 @@ __global__ void __launch_bounds__(kThreads) ar_reduce_norm_kernel(
       }
     }
   }
+}
+
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads) ar_push_kernel(const __nv_bfloat16* __restrict__ x, int T, int hidden,
+                                                           ArPeers peers, const uint32_t* epoch, uint32_t* ticket) {
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_launch_dependents();   // e.g. the next GEMM prefetches weights during our wait
+  const int p = (*epoch) & 1;
+  const int64_t n16 = (int64_t)T * hidden / 8;       // 16-byte vectors
+  const int64_t per = (n16 + gridDim.x - 1) / gridDim.x;
+  const int64_t v0 = blockIdx.x * per;
+  const int64_t v1 = min(n16, v0 + per);
+  const uint4* src = reinterpret_cast<const uint4*>(x);
+  for (int q = 0; q < push_dests(peers); ++q) {
+    uint4* dst = reinterpret_cast<uint4*>(push_slot(peers, q, p, hidden));
+    for (int64_t v = v0 + threadIdx.x; v < v1; v += blockDim.x) dst[v] = src[v];
+  }
+  publish_push(peers, p, ticket);
+}
+
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads) ar_reduce_norm_kernel(
+    int T, int hidden, ArPeers peers, uint32_t* epoch, uint32_t* ticket, uint32_t expected, float* residual,
+    const float* __restrict__ w, float eps, __nv_bfloat16* y, uint8_t* q, uint8_t* sf, uint32_t* err) {
+  __shared__ float red[32];
+  __shared__ int ok_s;
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_launch_dependents();   // e.g. the next GEMM prefetches weights during our wait
+  const int p = (*epoch) & 1;
+  uint8_t* mine = peers.base[peers.rank];
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const uint32_t* cnt = counters(mine, p);
+    const uint64_t t0 = globaltimer_ns();
+    for (int src = 0; src < peers.world && ok; ++src) {
+      while (ld_acquire_sys(cnt + src) < expected) {
+        if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+          atomicExch(err, kErrPeerTimeout);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    ok_s = ok;
+  }
+  __syncthreads();
+  if (ok_s && blockIdx.x < T)
+    row_add_norm_quant(blockIdx.x, hidden, recv_slot(mine, p, 0, peers.world, peers.max_t, hidden),
+                       (int64_t)peers.max_t * hidden, peers.world, residual, w, eps, y, q, sf, red);
   // completion: the last CTA resets this parity's counters and advances the epoch
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -267,8 +278,8 @@ __global__ void __launch_bounds__(kThreads) moe_combine_push_kernel(const __nv_b
     __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&outv);
 #pragma unroll
     for (int i = 0; i < 4; ++i) o[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
-    for (int q = 0; q < peers.world; ++q) {
-      __nv_bfloat16* dst = recv_slot(peers.base[q], p, peers.rank, peers.world, peers.max_t, hidden);
+    for (int q = 0; q < push_dests(peers); ++q) {
+      __nv_bfloat16* dst = push_slot(peers, q, p, hidden);
       *reinterpret_cast<uint4*>(dst + (int64_t)t * hidden + c) = outv;
     }
   }
@@ -284,5 +295,135 @@ int b200_moe_combine_push(const void* y, const int* pair_row, int T, int K, int 
   b200::launch_pdl(b200::comm::moe_combine_push_kernel, dim3(nctas), dim3(b200::comm::kThreads), 0, st, 
       reinterpret_cast<const __nv_bfloat16*>(y), pair_row, T, K, hidden, reinterpret_cast<const __nv_bfloat16*>(add),
       *peers, epoch, ticket);
+  return cudaGetLastError() == cudaSuccess ? 0 : 1;
+}
+
+// ---------------------------------------------------------------------------
+// NVLS all-reduce + residual + RMSNorm (+ MXFP8), one kernel of
+// G = min(T, kNvlsMaxCtas) CTAs, all co-resident (step 3 waits for every CTA
+// of every rank, so the grid never exceeds one CTA per SM).
+//
+//   1. wait until every rank's pusher published its arrival for this parity
+//      (the pushers stored their partial only into their own in[p] slot);
+//   2. this rank's share of the 16-byte vectors of the T x hidden sum:
+//      multimem.ld_reduce (the switch adds the same vector of every rank's
+//      in[p], fp32 accumulation) -> multimem.st into out[p] of every rank;
+//   3. each CTA publishes its share (P2P release increment of cnt_out[p][me]
+//      on every rank) and waits until every rank's G CTAs did;
+//   4. row epilogue on out[p] (local reads), as in the push reduction; CTA c
+//      takes rows c, c + G, ...
+// Bytes over NVLink per rank: one multicast read and one multicast write of
+// 1/world of the rows, versus (world - 1) full copies for the push.  Every
+// rank reads the same sums, so the outputs are identical on every rank.
+// Slot reuse follows the push protocol's argument: a rank pushes parity p
+// again only after its reduction of the other parity, which waited for every
+// rank's step 3 of this one.  The last CTA (ticket) zeroes both counter rows
+// of the parity and advances the epoch.
+namespace b200 {
+namespace comm {
+
+constexpr int kNvlsMaxCtas = 148;
+
+__device__ __forceinline__ void mm_ld_reduce_bf16x8(const void* mc, uint4& v) {
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(mc) : "memory");
+}
+__device__ __forceinline__ void mm_st_b128(void* mc, const uint4& v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1,%2,%3,%4};"
+               :: "l"(mc), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads) nvls_ar_norm_kernel(
+    int T, int hidden, ArPeers peers, uint32_t* epoch, uint32_t* ticket, uint32_t expected, float* residual,
+    const float* __restrict__ w, float eps, __nv_bfloat16* y, uint8_t* q, uint8_t* sf, uint32_t* err) {
+  __shared__ float red[32];
+  __shared__ int ok_s;
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  const int p = (*epoch) & 1;
+  uint8_t* mine = peers.base[peers.rank];
+  const int64_t slot = (int64_t)peers.max_t * hidden;                 // elements per slot
+  const int64_t in_off = kArRecvOff + (int64_t)p * slot * 2;           // bytes
+  const int64_t out_off = kArRecvOff + (int64_t)(2 + p) * slot * 2;
+  // 1. every rank's partial is in its in[p]
+  bool ok = wait_arrivals(mine, p, peers.world, expected, err, &ok_s);
+  // 2. this rank's share of the sum, broadcast through the switch
+  if (ok) {
+    const int64_t nvec = (int64_t)T * hidden / 8;
+    const int64_t per_rank = (nvec + peers.world - 1) / peers.world;
+    const int64_t r0 = peers.rank * per_rank, r1 = min(nvec, r0 + per_rank);
+    const int64_t per_cta = (r1 - r0 + gridDim.x - 1) / gridDim.x;
+    const int64_t c0 = r0 + blockIdx.x * per_cta, c1 = min(r1, c0 + per_cta);
+    const uint4* in_mc = reinterpret_cast<const uint4*>(peers.mc + in_off);
+    uint4* out_mc = reinterpret_cast<uint4*>(peers.mc + out_off);
+    for (int64_t v = c0 + threadIdx.x; v < c1; v += blockDim.x) {
+      uint4 s;
+      mm_ld_reduce_bf16x8(in_mc + v, s);
+      mm_st_b128(out_mc + v, s);
+    }
+  }
+  // 3. publish this CTA's share on every rank, then wait for all shares
+  __syncthreads();
+  if (threadIdx.x == 0 && ok) {
+    __threadfence_system();
+    for (int d = 0; d < peers.world; ++d)
+      asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(counters2(peers.base[d], p) + peers.rank), "r"(1u)
+                   : "memory");
+  }
+  if (threadIdx.x == 0) {
+    int ok2 = ok ? 1 : 0;
+    const uint32_t* cnt = counters2(mine, p);
+    const uint64_t t0 = globaltimer_ns();
+    for (int src = 0; src < peers.world && ok2; ++src) {
+      while (ld_acquire_sys(cnt + src) < (uint32_t)gridDim.x) {
+        if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+          atomicExch(err, kErrPeerTimeout);
+          ok2 = 0;
+          break;
+        }
+      }
+    }
+    ok_s = ok2;
+  }
+  __syncthreads();
+  // 4. row epilogue on the broadcast sum
+  if (ok_s)
+    for (int row = blockIdx.x; row < T; row += gridDim.x) {
+      row_add_norm_quant(row, hidden, reinterpret_cast<const __nv_bfloat16*>(mine + out_off), 0, 1, residual, w,
+                         eps, y, q, sf, red);
+      __syncthreads();                  // `red` is reused by the next row
+    }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t t = atomicAdd(ticket, 1u);
+    if (t == gridDim.x - 1) {
+      uint32_t* cnt = counters(mine, p);
+      uint32_t* cnt2 = counters2(mine, p);
+      for (int src = 0; src < peers.world; ++src) {
+        atomicExch(cnt + src, 0u);
+        atomicExch(cnt2 + src, 0u);
+      }
+      *ticket = 0u;
+      __threadfence();
+      atomicAdd(epoch, 1u);
+    }
+  }
+}
+
+}  // namespace comm
+}  // namespace b200
+
+int b200_nvls_ar_norm(int T, int hidden, const ArPeers* peers, uint32_t* epoch, uint32_t* ticket, int expected,
+                      float* residual, const float* w, float eps, void* y, uint8_t* q, uint8_t* sf, uint32_t* err,
+                      cudaStream_t st) {
+  if (T <= 0) return 0;
+  if (!peers->mc || T > peers->max_t || hidden % 32 || hidden > b200::comm::kThreads * 8 * b200::comm::kMaxIt ||
+      peers->world > kArMaxRanks || expected <= 0)
+    return -1;
+  const int G = T < b200::comm::kNvlsMaxCtas ? T : b200::comm::kNvlsMaxCtas;
+  b200::launch_pdl(b200::comm::nvls_ar_norm_kernel, dim3(G), dim3(b200::comm::kThreads), 0, st, T, hidden, *peers,
+                   epoch, ticket, (uint32_t)expected, residual, w, eps, reinterpret_cast<__nv_bfloat16*>(y), q, sf,
+                   err);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }

@@ -14,7 +14,21 @@ struct ArPeers {
   int max_t;                                // token rows per receive slot
   int hidden = 0;                           // bf16 columns per slot row (kernels that reuse the
                                             // slots as raw bytes need it to locate a slot)
+  // NVLS mode (nonzero `mc`, the multicast address of the same symmetric
+  // buffer): pushers store their partial only into their OWN input slot
+  // (layout of nvls_in_off) and still publish one arrival on every rank; the
+  // reduction then reads the sum of all ranks' slots through the switch.
+  uint8_t* mc = nullptr;
 };
+
+// NVLS all-reduce buffer (symmetric + multicast-bound, identical layout on
+// every rank):
+//   [0, 64)     uint32 cnt_in[2][kArMaxRanks]    pushers' arrivals
+//   [128, 192)  uint32 cnt_out[2][kArMaxRanks]   reduce CTAs done broadcasting
+//   kArRecvOff  bf16 in[2][max_t][hidden]        each rank's own partial
+//   then        bf16 out[2][max_t][hidden]       the sum, written by multimem.st
+constexpr int64_t kNvlsCnt2Off = 128;
+inline int64_t nvls_buffer_bytes(int max_t, int hidden) { return kArRecvOff + (int64_t)4 * max_t * hidden * 2; }
 
 inline int64_t ar_buffer_bytes(int world, int max_t, int hidden) {
   return kArRecvOff + (int64_t)2 * world * max_t * hidden * 2;
@@ -29,6 +43,13 @@ int b200_ar_reduce_norm(int T, int hidden, const ArPeers* peers, uint32_t* epoch
                         cudaStream_t st);
 int b200_moe_combine_push(const void* y, const int* pair_row, int T, int K, int hidden, const void* add,
                           const ArPeers* peers, const uint32_t* epoch, uint32_t* ticket, int nctas, cudaStream_t st);
+// NVLS all-reduce + residual + RMSNorm (+ MXFP8): waits for every rank's
+// push (`expected` arrivals each), sums this rank's share of the rows with
+// multimem.ld_reduce and broadcasts it with multimem.st, waits for every
+// rank's share, then the row epilogue of b200_ar_reduce_norm on the sum.
+int b200_nvls_ar_norm(int T, int hidden, const ArPeers* peers, uint32_t* epoch, uint32_t* ticket, int expected,
+                      float* residual, const float* w, float eps, void* y, uint8_t* q, uint8_t* sf, uint32_t* err,
+                      cudaStream_t st);
 
 // ---------------------------------------------------------------------------
 // Expert-parallel dispatch buffer (symmetric, identical layout on every rank):

@@ -29,6 +29,18 @@ __device__ __forceinline__ __nv_bfloat16* recv_slot(uint8_t* base, int parity, i
          ((int64_t)(parity * world + src) * max_t) * hidden;
 }
 
+// Destinations of a push: every rank's slot recv[parity][my rank] (push
+// mode), or only this rank's own NVLS input slot (mc set).
+__device__ __forceinline__ int push_dests(const ArPeers& p) { return p.mc ? 1 : p.world; }
+__device__ __forceinline__ __nv_bfloat16* push_slot(const ArPeers& p, int d, int parity, int hidden) {
+  return p.mc ? recv_slot(p.base[p.rank], parity, 0, 1, p.max_t, hidden)
+              : recv_slot(p.base[d], parity, p.rank, p.world, p.max_t, hidden);
+}
+
+__device__ __forceinline__ uint32_t* counters2(uint8_t* base, int parity) {
+  return reinterpret_cast<uint32_t*>(base + kNvlsCnt2Off) + parity * kArMaxRanks;
+}
+
 // Last CTA of the grid (by ticket) publishes one arrival on every rank.
 __device__ __forceinline__ void publish_push(uint8_t* const* bases, int world, int rank, int parity, uint32_t* ticket) {
   __syncthreads();

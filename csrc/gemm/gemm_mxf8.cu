@@ -400,9 +400,15 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
         for (int j = 0; j < 4; ++j) h2[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
         const int64_t oi = (int64_t)(b_row + col) * p.ldo + tile_n * kTileM + rr0;
         if constexpr (EPI == kEpiClusterPush) {
-          for (int dst = 0; dst < p.peers.world; ++dst) {
-            __nv_bfloat16* slot = reinterpret_cast<__nv_bfloat16*>(p.peers.base[dst] + kArRecvOff) +
-                                  ((int64_t)(parity * p.peers.world + p.peers.rank) * p.peers.max_t) * p.ldo;
+          // push mode: recv[parity][my rank] of every rank; NVLS mode (mc set):
+          // only this rank's own input slot in[parity]
+          const int nd = p.peers.mc ? 1 : p.peers.world;
+          for (int dst = 0; dst < nd; ++dst) {
+            __nv_bfloat16* slot =
+                p.peers.mc ? reinterpret_cast<__nv_bfloat16*>(p.peers.base[p.peers.rank] + kArRecvOff) +
+                                 (int64_t)parity * p.peers.max_t * p.ldo
+                           : reinterpret_cast<__nv_bfloat16*>(p.peers.base[dst] + kArRecvOff) +
+                                 ((int64_t)(parity * p.peers.world + p.peers.rank) * p.peers.max_t) * p.ldo;
             *reinterpret_cast<uint4*>(slot + oi) = v;
           }
         } else {

@@ -30,6 +30,10 @@ def _rank(rank, world, comm_impl, kind):
     from b200ds.models.loader import build_model
     from b200ds.models.reference import init_weights
     from b200ds.parallel.state import ParallelState, init_parallel
+    nvls = comm_impl == "nvls"
+    if nvls:      # the NVLS all-reduce (multicast) already at 2 ranks
+        os.environ["B200_NVLS_MIN_WORLD"] = "2"
+        comm_impl = "fused"
     ps = init_parallel(backend="nccl", timeout_s=60)
     ops.set_impl("native")
     # 32 heads: 16 per rank keeps both runs on the same tcgen05 MLA kernel
@@ -44,11 +48,20 @@ def _rank(rank, world, comm_impl, kind):
     m = build_model(cfg, ecfg, ps, sd, device=ps.device)
     m.allocate_kv(8)
     fb = _batch(cfg, ps.device)
-    out = m.forward(fb).float().cpu()
-    # device sampling without gathering the logits (candidates exchanged over
-    # the fused slots or NCCL): greedy rows must pick this run's argmax
-    z = torch.zeros(2, device=ps.device)
-    toks = m.forward_tokens(_batch(cfg, ps.device), z, z + 1, z.int(), z).cpu()
+    try:
+        out = m.forward(fb).float().cpu()
+        # device sampling without gathering the logits (candidates exchanged over
+        # the fused slots or NCCL): greedy rows must pick this run's argmax
+        z = torch.zeros(2, device=ps.device)
+        toks = m.forward_tokens(_batch(cfg, ps.device), z, z + 1, z.int(), z).cpu()
+    finally:
+        # both ranks finish their device work before either can leave (a rank
+        # must not exit while peers may still read its multicast-bound memory)
+        torch.cuda.synchronize()
+        import torch.distributed as dist
+        dist.barrier(group=ps.cpu_group)
+    if nvls:
+        assert ps.fused_ar is not None and ps.fused_ar.nvls is not None, "NVLS buffer not set up"
     assert toks.tolist() == out.argmax(-1).tolist(), (toks, out.argmax(-1))
     ref = None
     if rank == 0:
@@ -84,15 +97,26 @@ def _rel(a, b):
     return ((a - b).norm() / b.norm()).item()
 
 
-@pytest.mark.parametrize("comm_impl", ["nccl", "fused"])
+def _has_multicast():
+    try:
+        import torch.distributed._symmetric_memory as sm
+        return bool(sm._SymmetricMemory.has_multicast_support(sm.DeviceType.CUDA, 0))
+    except Exception:
+        return False
+
+
+@pytest.mark.parametrize("comm_impl", ["nccl", "fused", "nvls"])
 @pytest.mark.parametrize("kind,tol", [("dense", 2e-2), ("moe", 1e-1)])
 def test_tp2_ep2_matches_single_gpu(comm_impl, kind, tol):
     """TP2/EP2 vs one GPU.  The runs differ only in how partial sums are
     rounded (bf16 partials, then summed), but every later MXFP8 quantization
     can turn such a difference into a flipped e4m3 code or UE8M0 block scale,
     so the error compounds with depth: the 1-layer dense model is held
-    tightly, the 4-layer MoE model loosely.  Both ranks must agree exactly."""
+    tightly, the 4-layer MoE model loosely.  Both ranks must agree exactly.
+    "nvls": the all-reduces run through NVLink multicast (multimem) on 2 ranks."""
     _needs(2)
+    if comm_impl == "nvls" and not _has_multicast():
+        pytest.skip("no NVLink multicast on this box")
     res = run_ranks(_rank, 2, comm_impl, kind, timeout=600)
     out0, ref = res[0]
     out1, _ = res[1]
