@@ -111,7 +111,9 @@ class DecodeGraphRunner:
 
     def capture(self, bs: int) -> _Graph:
         g = self._make_static(bs)
-        s = torch.cuda.Stream(device=self.dev)
+        # the main chain is captured from a high-priority stream (its kernel
+        # nodes keep the priority): side-stream prefetches yield to it
+        s = torch.cuda.Stream(device=self.dev, priority=-2)
         s.wait_stream(torch.cuda.current_stream(self.dev))
         with torch.cuda.stream(s):
             for _ in range(2):

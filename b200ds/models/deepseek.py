@@ -141,7 +141,8 @@ class DeepseekModel:
                 and getattr(ps, "fused_ep", None) is None):
             from ..parallel.symm import EPDispatch, FusedAllReduce
             cap = max(ecfg.max_num_seqs, 256)
-            ps.fused_ar = FusedAllReduce(ps, cfg.hidden_size, max_tokens=cap, group="ep")
+            ps.fused_ar = FusedAllReduce(ps, cfg.hidden_size, max_tokens=cap, group="ep",
+                                         topk=cfg.num_experts_per_tok)
             ps.fused_ep = EPDispatch(ps, cfg.hidden_size, cfg.num_experts_per_tok, cap)
 
     # ------------------------------------------------------------------
@@ -187,11 +188,14 @@ class DeepseekModel:
         topk = None
         if c.index_n_heads:
             topk = self._indexer(i, aw, qkv, qo, fb)
+        # weights the layer streams after attention go to L2 meanwhile
+        self._prefetch(i, lw, fb)
         # absorption of q_nope into the latent space, RoPE of the (un-rotated)
         # rope part and the e4m3 query prep run fused ahead of the attention
         o_lat = ops.mla_from_q(q[..., : c.qk_nope_head_dim], q[..., c.qk_nope_head_dim:], aw.w_uk,
                                getattr(aw, "w_uk_t", None), self.kv_cache[i], self.kv_scale[i], fb,
                                c.softmax_scale, self.page_size, topk, self.rope_table)
+        self._prefetch_join()
         o = ops.absorb_o(o_lat, aw.w_uv, quantize=aw.o_proj.quantized)   # [T, Hl*v] (MXFP8 when quantized)
         if self.device.type == "cuda" and self.attn_tp > 1:
             # leave the o_proj GEMM to the all-reduce so it can run fused
@@ -264,7 +268,7 @@ class DeepseekModel:
                 shared = self._fork(lambda: mw.shared_down(ops.gate_up_swiglu(h, mw.shared_gate_up),
                                                            out_dtype=out_dt), h)
             w, ids = ops.router(h, mw.gate, mw.bias, c)
-            part = ops.moe_experts_ep(h, w, ids, mw.experts, T_step, c.n_routed_experts, ep)
+            part = ops.moe_experts_ep(h, w, ids, mw.experts, T_step, c.n_routed_experts, ep, far)
             if shared is not None:
                 part.add = self._join(shared)
             return part
@@ -281,12 +285,50 @@ class DeepseekModel:
         return out.to(out_dt)
 
     # ------------------------------------------------------------------
+    L2_PREFETCH_LIMIT = 24 << 20        # bytes per region (L2 is 126 MB; attention reads the KV meanwhile)
+
+    def _prefetch(self, i: int, lw, fb) -> None:
+        """Decode steps: issue L2 prefetches of the o-projection weights and
+        (MoE layers) the shared expert's gate_up on a low-priority side stream
+        that runs next to the attention kernels; `_prefetch_join` rejoins it
+        before the o-projection.  The reference warms WO-A / wo_b / the router
+        the same way (l2pf.py:4-5, l2pf_unit.cu:22,33)."""
+        self._pf_live = False
+        if not (self.device.type == "cuda" and fb.is_decode and ops.get_impl() == "native"):
+            return
+        from ..utils import levers
+        if not levers.on("l2_prefetch"):
+            return
+        ts = []
+        for lin in (lw.attn.o_proj, getattr(lw.ffn, "shared_gate_up", None)):
+            w = getattr(lin, "w", lin)
+            data = getattr(w, "data", None)
+            if isinstance(data, torch.Tensor) and data.is_cuda and data.is_contiguous():
+                ts.append(data.view(torch.uint8))
+        if not ts:
+            return
+        from .. import _C
+        main = torch.cuda.current_stream(self.device)
+        if getattr(self, "_pf", None) is None:
+            self._pf = torch.cuda.Stream(device=self.device, priority=0)     # lowest priority
+        self._pf.wait_stream(main)
+        with torch.cuda.stream(self._pf):
+            _C.l2_prefetch(ts, self.L2_PREFETCH_LIMIT, 32)
+        self._pf_live = True
+
+    def _prefetch_join(self) -> None:
+        if getattr(self, "_pf_live", False):
+            torch.cuda.current_stream(self.device).wait_stream(self._pf)
+            self._pf_live = False
+
     def _fork(self, fn, *inputs):
         """Run fn() on the side stream after the main stream's pending work;
         returns a handle for `_join`."""
         main = torch.cuda.current_stream(self.device)
         if getattr(self, "_side", None) is None:
-            self._side = torch.cuda.Stream(device=self.device)
+            # highest priority: the shared expert is short and joins the MoE
+            # combine, so its kernels go ahead of the routed experts' CTAs
+            self._side = torch.cuda.Stream(device=self.device, priority=-5)
         side = self._side
         side.wait_stream(main)
         with torch.cuda.stream(side):

@@ -70,6 +70,13 @@ class V4LayerWeights:
     engram: Optional[EngramWeights] = None
 
 
+@dataclass
+class _Partial:
+    """A sublayer output that is still this rank's partial sum (tensor
+    parallelism): its all-reduce runs fused with the hyper-connection post."""
+    y: torch.Tensor
+
+
 class DeepseekV4Model:
     def __init__(self, cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState, layers: List[V4LayerWeights],
                  embed: torch.Tensor, hc_head: HcWeights, final_ln: torch.Tensor, lm_head, device,
@@ -101,6 +108,15 @@ class DeepseekV4Model:
         from ..ops.ref import engram_multipliers
         m = [v - (1 << 64) if v >= (1 << 63) else v for v in engram_multipliers(max(cfg.engram_heads, 1))]
         self.engram_mults = torch.tensor(m, dtype=torch.int64, device=self.device)
+        # tensor parallelism on GPUs: each sublayer's all-reduce runs fused
+        # with the hyper-connection post (csrc/elementwise/v4.cu ar_hc_post)
+        from ..utils import levers
+        if (self.device.type == "cuda" and ps.tp_size > 1 and not self.dp and ecfg.comm_impl == "fused"
+                and levers.on("fused_comm") and getattr(ps, "fused_ar", None) is None):
+            from ..parallel.symm import FusedAllReduce
+            # the V4 boundary kernel reads the push protocol's per-source slots
+            ps.fused_ar = FusedAllReduce(ps, cfg.hidden_size, max_tokens=max(ecfg.max_num_seqs, 256),
+                                         allow_nvls=False)
 
     # ------------------------------------------------------------------
     def allocate_kv(self, num_pages: int):
@@ -139,9 +155,24 @@ class DeepseekV4Model:
     def _out_dtype(self):
         return torch.float32 if self.device.type == "cpu" else torch.bfloat16
 
+    def _fused_post(self, T: int) -> bool:
+        """The sublayer all-reduce is left to the fused all-reduce + hc_post."""
+        far = getattr(self.ps, "fused_ar", None)
+        return (far is not None and not self.dp and self.ps.tp_size > 1 and ops.get_impl() == "native"
+                and far.supports(T))
+
+    def _post(self, X, y, post, comb):
+        """hc_post of a sublayer output y (a rank partial when the fused
+        boundary runs, else already reduced); returns the row sum of squares."""
+        if isinstance(y, _Partial):
+            return self.ps.fused_ar.allreduce_hc_post(y.y, X, post, comb)
+        return ops.hc_post(X, y, post, comb)
+
     def _reduce(self, y: torch.Tensor) -> torch.Tensor:
         if self.dp:                 # replicated weights, this rank's own tokens: nothing to sum
             return y
+        if self._fused_post(y.shape[0]):
+            return _Partial(y)
         if self.ps.tp_size > 1:
             self.ps.tp_all_reduce(y)
         elif self.ps.ep_size > 1:
@@ -248,7 +279,7 @@ class DeepseekV4Model:
         for i, lw in enumerate(self.layers):
             tr.mark(f"L{i}.attn")
             if carry is not None:
-                ss = ops.hc_post(X, *carry)
+                ss = self._post(X, *carry)
             if i == c.late_layer_start and fb.tail_from is not None:
                 # prefill tail: the window-only layers need only the rows within
                 # reach of each prompt's end (ForwardBatch.tail_rows)
@@ -263,14 +294,14 @@ class DeepseekV4Model:
                 self.aux.append(ops.hc_mean(X))
             h, post, comb = ops.hc_pre(X, ss, lw.attn_hc, lw.in_ln, eps, c, lw.attn.wqkv_a)
             y = self._attention(i, lw, h, fb)
-            ss = ops.hc_post(X, y, post, comb)
+            ss = self._post(X, y, post, comb)
             tr.mark(f"L{i}.ffn")
             moe = isinstance(lw.ffn, MoEWeights)
             h, post, comb = ops.hc_pre(X, ss, lw.ffn_hc, lw.post_ln, eps, c, self._ffn_first_linear(lw),
                                        keep_hf=moe)
             carry = (self._ffn(i, lw, h, fb), post, comb)
         tr.mark("head")
-        ss = ops.hc_post(X, *carry)
+        ss = self._post(X, *carry)
         h, _, _ = ops.hc_pre(X, ss, self.hc_head, self.final_ln, eps, c, None, head=True)
         return h, fb
 

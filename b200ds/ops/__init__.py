@@ -101,11 +101,16 @@ class EPPartial:
     row index pair_row [world * T_step, K], this rank's T_r own tokens and an
     optional additive partial for them (shared expert).  Consumed by the
     fused reduce-scatter + residual + RMSNorm."""
-    y: torch.Tensor
+    y: Optional[torch.Tensor]
     pair_row: torch.Tensor
     T_step: int
     T_r: int
     add: Optional[torch.Tensor] = None
+    # combine already stored by the experts' FC2 epilogue into the owners'
+    # slots (y unused): the owner sums its tokens' K pair rows (ids [T_r, K],
+    # < 0 = no expert)
+    pushed: bool = False
+    ids: Optional[torch.Tensor] = None
 
 
 def materialize(a, out_dtype=torch.bfloat16) -> torch.Tensor:
@@ -353,11 +358,13 @@ def router(h, gate: torch.Tensor, bias: torch.Tensor, cfg):
 
 
 def moe_experts_ep(h, w: torch.Tensor, ids: torch.Tensor, ex: ExpertWeights, T_step: int, n_experts_total: int,
-                   ep) -> EPPartial:
+                   ep, far=None) -> EPPartial:
     """Expert-parallel MoE on the fused NVLink path: dispatch this rank's
     routed tokens to the expert owners, run the grouped GEMMs over the
-    received tokens; returns the partial for the fused combine."""
-    return _native().moe_experts_ep(h, w, ids, ex, T_step, n_experts_total, ep)
+    received tokens; returns the partial for the fused combine (with `far`,
+    the expert-parallel all-reduce workspace, the FC2 epilogue stores each
+    pair's row straight into its owner's slot)."""
+    return _native().moe_experts_ep(h, w, ids, ex, T_step, n_experts_total, ep, far)
 
 
 def moe_experts(h, w: torch.Tensor, ids: torch.Tensor, ex: ExpertWeights, out_dtype=torch.float32,

@@ -103,6 +103,8 @@ def allreduce_add_rmsnorm(a, residual, w, eps, ps, next_linear=None):
         quantized = next_linear is not None and getattr(next_linear, "quantized", False)
         if residual.dtype != torch.float32:
             residual = residual.float()
+        if a.pushed:
+            return far.ep_comb_add_rmsnorm(a, residual, w, eps, quantized)
         return far.ep_rs_add_rmsnorm(a, residual, w, eps, quantized)
     if far is not None and far.supports(T):
         quantized = next_linear is not None and getattr(next_linear, "quantized", False)
@@ -524,7 +526,7 @@ def moe_experts_nvfp4(h, w, ids, ex, out_dtype=torch.bfloat16, n_experts_total=N
     return out
 
 
-def moe_experts_ep(h, w, ids, ex, T_step: int, n_experts_total: int, ep):
+def moe_experts_ep(h, w, ids, ex, T_step: int, n_experts_total: int, ep, far=None):
     """Expert-parallel MoE: ep_dispatch (P2P push of routed rows) -> ep_align
     (bounded wait + routing layout over all ranks' tokens) -> persistent
     FC1 (SwiGLU + requant; its producer reads the received rows in place) ->
@@ -563,14 +565,22 @@ def moe_experts_ep(h, w, ids, ex, T_step: int, n_experts_total: int, ep):
     pair_row = torch.empty(Tg, K, dtype=torch.int32, device=dev)
     total = torch.empty(1, dtype=torch.int32, device=dev)
     pulls = _pulls(bn1, bn2)
+    # the combine fused into the FC2 epilogue (pair rows stored straight into
+    # the owners' slots of the expert-parallel all-reduce workspace)
+    comb = (pulls and far is not None and getattr(far, "topk", 0) == K and far.supports(T_step)
+            and levers.on("ep_combine_epilogue"))
+    row_pair = torch.empty(max_rows, dtype=torch.int32, device=dev) if comb else None
     _C.ep_align(ep.bases, ep.rank, ep.max_t, Hd, K, T_step, ex.first, E, seg_start, seg_count, row_token, row_weight,
-                pair_row, total, bn1, tt1, bn2, tt2, ep.epoch, ep.err, release=pulls)
-    y = torch.empty(max_rows, Hd, dtype=torch.bfloat16, device=dev)
+                pair_row, total, bn1, tt1, bn2, tt2, ep.epoch, ep.err, release=pulls, row_pair=row_pair)
+    y = torch.empty(max_rows if not comb else 1, Hd, dtype=torch.bfloat16, device=dev)
     if pulls:
         # received rows read in place (row index = owner rank * T_step + t);
         # ep_align advanced the epoch, so they sit at parity (epoch + 1) & 1
         pull = dict(row_token=row_token, src_q=[ep.recv_q], src_sf=[ep.recv_sf], src_g=[ep.recv_g] if fp4 else [],
                     src_rows=ep.world * ep.max_t, src_epoch=ep.epoch, src_epoch_add=1, src_par_bytes=ep.par_bytes)
+        if comb:
+            pull.update(c_row_pair=row_pair, c_K=K, c_T_step=T_step, c_bases=far.bases, c_rank=far.rank,
+                        c_max_t=far.max_tokens, c_off=far.comb_off, c_epoch=far.epoch)
         if fp4:
             hq = torch.empty(max_rows, I // 2, dtype=torch.uint8, device=dev)
             hsf = torch.empty(max_rows * (I // 16), dtype=torch.uint8, device=dev)
@@ -579,6 +589,8 @@ def moe_experts_ep(h, w, ids, ex, T_step: int, n_experts_total: int, ep):
             hq, hsf = h_.q, h_.sf
         _expert_gemms(ex, None, None, None, hq, hsf, y, Hd, bn1, bn2, seg_start, seg_count, tt1, tt2, row_weight, fp4,
                       pull)
+        if comb:
+            return EPPartial(None, pair_row, T_step, T_r, pushed=True, ids=ids[:T_r].contiguous())
         return EPPartial(y, pair_row, T_step, T_r)
     if fp4:
         xs_q = torch.empty(max_rows, Hd // 2, dtype=torch.uint8, device=dev)

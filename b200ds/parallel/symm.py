@@ -26,7 +26,8 @@ import torch.distributed as dist
 
 
 class FusedAllReduce:
-    def __init__(self, ps, hidden: int, max_tokens: int = 256, push_ctas: int = 296, group: str = "tp"):
+    def __init__(self, ps, hidden: int, max_tokens: int = 256, push_ctas: int = 296, group: str = "tp",
+                 allow_nvls: bool = True, topk: int = 0):
         import torch.distributed._symmetric_memory as symm_mem
         from .. import _C
         self.ps = ps
@@ -42,7 +43,12 @@ class FusedAllReduce:
         name = group.group_name
         if hasattr(symm_mem, "enable_symm_mem_for_group") and not symm_mem.is_symm_mem_enabled_for_group(name):
             symm_mem.enable_symm_mem_for_group(name)
-        nbytes = int(_C.ar_buffer_size(self.world, max_tokens, hidden))
+        # expert-parallel workspaces also hold the combine region the experts'
+        # FC2 epilogues write into ([2][max_tokens][topk][hidden] bf16)
+        self.topk = topk
+        nbytes = int(_C.ep_ar_buffer_size(self.world, max_tokens, hidden, topk) if topk > 0
+                     else _C.ar_buffer_size(self.world, max_tokens, hidden))
+        self.comb_off = int(_C.ep_combine_offset(self.world, max_tokens, hidden)) if topk > 0 else 0
         self.buf = symm_mem.empty(nbytes, dtype=torch.uint8, device=dev)
         self.buf.zero_()
         self.hdl = symm_mem.rendezvous(self.buf, name)
@@ -54,7 +60,7 @@ class FusedAllReduce:
         # NVLS only for the tensor-parallel all-reduce (the expert-parallel
         # reduce-scatter keeps the push protocol)
         self.nvls = (_Nvls.create(ps, name, group, self.world, self.rank, max_tokens, hidden, dev)
-                     if self.world > 1 and is_tp else None)
+                     if self.world > 1 and is_tp and allow_nvls else None)
         torch.cuda.synchronize(dev)
         dist.barrier(group=group)
 
@@ -135,6 +141,23 @@ class FusedAllReduce:
         y, qa = self._outs(T, H, part.y.device, quantize)
         return self._reduce(T, H, 1, residual, ln_w, eps, y, qa)
 
+    def ep_comb_add_rmsnorm(self, part, residual, ln_w, eps, quantize):
+        """Expert-parallel combine whose pair rows the experts' FC2 epilogues
+        already stored into this rank's combine slots: one kernel sums each
+        own token's K rows + its shared-expert row + the residual, RMSNorm,
+        quant."""
+        from .. import _C
+        H = self.hidden
+        add = part.add.to(torch.bfloat16).contiguous() if part.add is not None else None
+        y, qa = self._outs(part.T_r, H, residual.device, quantize)
+        _C.ep_comb_reduce_norm(part.T_r, H, part.ids.shape[1], part.ids, add, self.bases, self.rank, self.max_tokens,
+                               self.epoch, self.ticket, residual, ln_w, eps, y, qa.q if qa else None,
+                               qa.sf if qa else None, self.err)
+        if qa is not None:
+            qa.hf = y
+            return qa, residual
+        return y, residual
+
     def ep_rs_add_rmsnorm(self, part, residual, ln_w, eps, quantize):
         """Expert-parallel combine: each received token's partial goes to its
         owner's slot (reduce-scatter), then this rank's reduce + residual +
@@ -146,6 +169,20 @@ class FusedAllReduce:
                          self.epoch, self.push_ticket, self.push_ctas)
         y, qa = self._outs(part.T_r, H, part.y.device, quantize)
         return self._reduce(part.T_r, H, 1, residual, ln_w, eps, y, qa, nvls=False)
+
+    def allreduce_hc_post(self, y: torch.Tensor, X: torch.Tensor, post: torch.Tensor, comb: torch.Tensor):
+        """DeepSeek-V4 sublayer boundary: y (this rank's partial [T, D]) is
+        pushed into every rank's slot, then one kernel sums the partials and
+        applies the hyper-connection post to X in place; returns the row sum
+        of squares of the new streams."""
+        from .. import _C
+        T, D = y.shape
+        x = y if (y.dtype == torch.bfloat16 and y.is_contiguous()) else y.to(torch.bfloat16).contiguous()
+        _C.ar_push(x, self.bases, self.rank, self.max_tokens, self.epoch, self.push_ticket, self.push_ctas)
+        ss = torch.empty(T, dtype=torch.float32, device=y.device)
+        _C.ar_hc_post(T, D, self.bases, self.rank, self.max_tokens, self.epoch, self.ticket, 1, X, post, comb, ss,
+                      self.err)
+        return ss
 
     def check(self) -> None:
         """Raise if a bounded wait inside the kernels timed out."""

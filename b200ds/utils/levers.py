@@ -123,6 +123,12 @@ register("fused_comm", "B200_FUSED_COMM", True,
 register("nvls", "B200_NVLS", True,
          "tensor-parallel all-reduces through NVLink multicast (multimem.ld_reduce / multimem.st in the switch) on "
          "groups of B200_NVLS_MIN_WORLD (default 4) or more ranks with multicast support")
+register("l2_prefetch", "B200_L2_PREFETCH", True,
+         "decode layers pull the o-projection (and shared-expert) weights into L2 on a low-priority side stream "
+         "while attention runs")
+register("ep_combine_epilogue", "B200_EP_COMBINE_EPILOGUE", True,
+         "expert parallelism: the experts' FC2 epilogue stores each weighted pair row straight into its token's "
+         "owner rank (no separate combine kernel, no local round trip of the FC2 rows)")
 register("deterministic", "B200_DETERMINISTIC", False,
          "bitwise-reproducible steps: split-K GEMMs that sum with fp32 atomics (router logits, mHC stats) run "
          "unsplit")

@@ -302,7 +302,9 @@ void moe_fused(const at::Tensor& w13, const at::Tensor& w13_sf, const at::Tensor
                int64_t num_ctas, bool pdl, bool a_tiled, c10::optional<at::Tensor> x_g, c10::optional<at::Tensor> w1_g,
                c10::optional<at::Tensor> w2_g, double out_g, c10::optional<at::Tensor> row_token,
                std::vector<int64_t> src_q, std::vector<int64_t> src_sf, std::vector<int64_t> src_g, int64_t src_rows,
-               c10::optional<at::Tensor> src_epoch, int64_t src_epoch_add, int64_t src_par_bytes) {
+               c10::optional<at::Tensor> src_epoch, int64_t src_epoch_add, int64_t src_par_bytes,
+               c10::optional<at::Tensor> c_row_pair, int64_t c_K, int64_t c_T_step, std::vector<int64_t> c_bases,
+               int64_t c_rank, int64_t c_max_t, int64_t c_off, c10::optional<at::Tensor> c_epoch) {
   check_cuda(w13, "w13");
   const c10::cuda::CUDAGuard gd(w13.device());
   TORCH_CHECK(ws.scalar_type() == at::kInt && ws.numel() >= 2 + E, "workspace int32 [2 + E]");
@@ -360,6 +362,19 @@ void moe_fused(const at::Tensor& w13, const at::Tensor& w13_sf, const at::Tensor
       a.src_par_bytes = src_par_bytes;
     }
     a.rows = hq.size(0);
+  }
+  // expert-parallel combine stored by the FC2 epilogue into the owners' slots
+  if (c_row_pair.has_value() && c_row_pair->defined()) {
+    TORCH_CHECK(!c_bases.empty() && c_bases.size() <= 8 && c_epoch.has_value(), "combine: 1..8 rank bases + epoch");
+    a.c_row_pair = ptr<int>(*c_row_pair);
+    a.c_K = int(c_K);
+    a.c_T_step = int(c_T_step);
+    for (size_t i = 0; i < c_bases.size(); ++i) a.c_base[i] = reinterpret_cast<uint8_t*>(c_bases[i]);
+    a.c_rank = int(c_rank);
+    a.c_world = int(c_bases.size());
+    a.c_max_t = int(c_max_t);
+    a.c_off = c_off;
+    a.c_epoch = reinterpret_cast<const uint32_t*>(c_epoch->data_ptr());
   }
   check(b200_moe_fused(&a, cur_stream()), "moe_fused");
 }
@@ -468,7 +483,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("src_q") = std::vector<int64_t>{}, pybind11::arg("src_sf") = std::vector<int64_t>{},
         pybind11::arg("src_g") = std::vector<int64_t>{}, pybind11::arg("src_rows") = 0,
         pybind11::arg("src_epoch") = pybind11::none(), pybind11::arg("src_epoch_add") = 0,
-        pybind11::arg("src_par_bytes") = 0);
+        pybind11::arg("src_par_bytes") = 0, pybind11::arg("c_row_pair") = pybind11::none(), pybind11::arg("c_K") = 0,
+        pybind11::arg("c_T_step") = 0, pybind11::arg("c_bases") = std::vector<int64_t>{}, pybind11::arg("c_rank") = 0,
+        pybind11::arg("c_max_t") = 0, pybind11::arg("c_off") = 0, pybind11::arg("c_epoch") = pybind11::none());
   m.def("moe_gather4", &moe_gather4);
   m.def("num_sms", &num_sms);
   m.def("graph_kernel_count", &graph_kernel_count);

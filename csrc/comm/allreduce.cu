@@ -46,13 +46,17 @@ __device__ __forceinline__ void publish_push(const ArPeers& peers, int parity, u
 }
 
 
-// Row epilogue shared by the push and NVLS reductions: v = sum of the nsrc
-// bf16 rows (src0 + i * src_stride, in index order) + residual (updated in
-// place, fp32); RMSNorm; bf16 y and / or MXFP8 q + sf (tcgen05 scale layout).
-// One CTA of kThreads per row; `red` is >= 32 floats of shared memory.
+// Row epilogue shared by the push, NVLS and expert-combine reductions: v =
+// sum of the nsrc bf16 rows src0 + row * row_stride + i * src_stride (in
+// index order; source i skipped when ids_row[i] < 0) + add_row (optional) +
+// residual (updated in place, fp32); RMSNorm; bf16 y and / or MXFP8 q + sf
+// (tcgen05 scale layout).  One CTA of kThreads per row; `red` is >= 32
+// floats of shared memory.
 __device__ __forceinline__ void row_add_norm_quant(int row, int hidden, const __nv_bfloat16* src0, int64_t src_stride,
-                                                   int nsrc, float* residual, const float* __restrict__ w, float eps,
-                                                   __nv_bfloat16* y, uint8_t* q, uint8_t* sf, float* red) {
+                                                   int nsrc, int64_t row_stride, const int* ids_row,
+                                                   const __nv_bfloat16* add_row, float* residual,
+                                                   const float* __restrict__ w, float eps, __nv_bfloat16* y,
+                                                   uint8_t* q, uint8_t* sf, float* red) {
   const int units = hidden >> 3;
   {
     float v[kMaxIt][8];
@@ -64,8 +68,19 @@ __device__ __forceinline__ void row_add_norm_quant(int row, int hidden, const __
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[it][i] = 0.f;
         for (int src = 0; src < nsrc; ++src) {
-          const __nv_bfloat16* s = src0 + src * src_stride + (int64_t)row * hidden;
+          if (ids_row && __ldcg(ids_row + src) < 0) continue;
+          const __nv_bfloat16* s = src0 + src * src_stride + (int64_t)row * row_stride;
           const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(s + u * 8));
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h[i]);
+            v[it][2 * i] += f.x;
+            v[it][2 * i + 1] += f.y;
+          }
+        }
+        if (add_row) {
+          const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(add_row + u * 8));
           const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -189,7 +204,8 @@ __global__ void __launch_bounds__(kThreads) ar_reduce_norm_kernel(
   __syncthreads();
   if (ok_s && blockIdx.x < T)
     row_add_norm_quant(blockIdx.x, hidden, recv_slot(mine, p, 0, peers.world, peers.max_t, hidden),
-                       (int64_t)peers.max_t * hidden, peers.world, residual, w, eps, y, q, sf, red);
+                       (int64_t)peers.max_t * hidden, peers.world, hidden, nullptr, nullptr, residual, w, eps, y, q,
+                       sf, red);
   // completion: the last CTA resets this parity's counters and advances the epoch
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -389,8 +405,8 @@ __global__ void __launch_bounds__(kThreads) nvls_ar_norm_kernel(
   // 4. row epilogue on the broadcast sum
   if (ok_s)
     for (int row = blockIdx.x; row < T; row += gridDim.x) {
-      row_add_norm_quant(row, hidden, reinterpret_cast<const __nv_bfloat16*>(mine + out_off), 0, 1, residual, w,
-                         eps, y, q, sf, red);
+      row_add_norm_quant(row, hidden, reinterpret_cast<const __nv_bfloat16*>(mine + out_off), 0, 1, hidden, nullptr,
+                         nullptr, residual, w, eps, y, q, sf, red);
       __syncthreads();                  // `red` is reused by the next row
     }
   __syncthreads();
@@ -425,5 +441,62 @@ int b200_nvls_ar_norm(int T, int hidden, const ArPeers* peers, uint32_t* epoch, 
   b200::launch_pdl(b200::comm::nvls_ar_norm_kernel, dim3(G), dim3(b200::comm::kThreads), 0, st, T, hidden, *peers,
                    epoch, ticket, (uint32_t)expected, residual, w, eps, reinterpret_cast<__nv_bfloat16*>(y), q, sf,
                    err);
+  return cudaGetLastError() == cudaSuccess ? 0 : 1;
+}
+
+// ---------------------------------------------------------------------------
+// Owner side of the expert-parallel combine fused into the experts' FC2
+// epilogue (moe_fused.cu): every rank stored the weighted output row of each
+// pair (t, k) it served straight into comb[p][t][k] of t's owner and
+// published one arrival.  One CTA per own token row: wait (bounded) for every
+// rank's arrival, sum the row's K pair rows in k order (pairs whose expert id
+// is < 0 were pruned / padded and are skipped) + the shared-expert row, add
+// the residual, RMSNorm (+ MXFP8).  The last CTA zeroes the parity's
+// counters and advances the epoch (the push reduction's protocol).
+namespace b200 {
+namespace comm {
+__global__ void __launch_bounds__(kThreads) ep_comb_reduce_norm_kernel(
+    int T_r, int hidden, int K, const int* __restrict__ ids, const __nv_bfloat16* __restrict__ add, ArPeers peers,
+    uint32_t* epoch, uint32_t* ticket, float* residual, const float* __restrict__ w, float eps, __nv_bfloat16* y,
+    uint8_t* q, uint8_t* sf, uint32_t* err) {
+  __shared__ float red[32];
+  __shared__ int ok_s;
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  const int p = (*epoch) & 1;
+  uint8_t* mine = peers.base[peers.rank];
+  const bool ok = wait_arrivals(mine, p, peers.world, 1u, err, &ok_s);
+  const int row = blockIdx.x;
+  if (ok && row < T_r) {
+    const __nv_bfloat16* comb = reinterpret_cast<const __nv_bfloat16*>(
+        mine + ep_combine_off(peers.world, peers.max_t, hidden) + (int64_t)p * peers.max_t * K * hidden * 2);
+    row_add_norm_quant(row, hidden, comb, hidden, K, (int64_t)K * hidden, ids + (int64_t)row * K,
+                       add ? add + (int64_t)row * hidden : nullptr, residual, w, eps, y, q, sf, red);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t t = atomicAdd(ticket, 1u);
+    if (t == gridDim.x - 1) {
+      uint32_t* cnt = counters(mine, p);
+      for (int src = 0; src < peers.world; ++src) atomicExch(cnt + src, 0u);
+      *ticket = 0u;
+      __threadfence();
+      atomicAdd(epoch, 1u);
+    }
+  }
+}
+}  // namespace comm
+}  // namespace b200
+
+int b200_ep_comb_reduce_norm(int T_r, int hidden, int K, const int* ids, const void* add, const ArPeers* peers,
+                             uint32_t* epoch, uint32_t* ticket, float* residual, const float* w, float eps, void* y,
+                             uint8_t* q, uint8_t* sf, uint32_t* err, cudaStream_t st) {
+  if (T_r <= 0) return 0;
+  if (T_r > peers->max_t || hidden % 32 || hidden > b200::comm::kThreads * 8 * b200::comm::kMaxIt || K <= 0)
+    return -1;
+  b200::launch_pdl(b200::comm::ep_comb_reduce_norm_kernel, dim3(T_r), dim3(b200::comm::kThreads), 0, st, T_r, hidden,
+                   K, ids, reinterpret_cast<const __nv_bfloat16*>(add), *peers, epoch, ticket, residual, w, eps,
+                   reinterpret_cast<__nv_bfloat16*>(y), q, sf, err);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }

@@ -30,8 +30,17 @@ struct ArPeers {
 constexpr int64_t kNvlsCnt2Off = 128;
 inline int64_t nvls_buffer_bytes(int max_t, int hidden) { return kArRecvOff + (int64_t)4 * max_t * hidden * 2; }
 
-inline int64_t ar_buffer_bytes(int world, int max_t, int hidden) {
+__host__ __device__ inline int64_t ar_buffer_bytes(int world, int max_t, int hidden) {
   return kArRecvOff + (int64_t)2 * world * max_t * hidden * 2;
+}
+// Expert-parallel buffers (DP attention) append a combine region after the
+// per-source slots: bf16 comb[2][max_t][K][hidden], filled by the experts'
+// FC2 epilogues of every rank (pair (t, k) of this rank's token t).
+__host__ __device__ inline int64_t ep_combine_off(int world, int max_t, int hidden) {
+  return ar_buffer_bytes(world, max_t, hidden);
+}
+inline int64_t ar_buffer_bytes_ep(int world, int max_t, int hidden, int K) {
+  return ep_combine_off(world, max_t, hidden) + (int64_t)2 * max_t * K * hidden * 2;
 }
 
 // Push kernels publish once per destination rank (the last CTA, by ticket);
@@ -50,6 +59,18 @@ int b200_moe_combine_push(const void* y, const int* pair_row, int T, int K, int 
 int b200_nvls_ar_norm(int T, int hidden, const ArPeers* peers, uint32_t* epoch, uint32_t* ticket, int expected,
                       float* residual, const float* w, float eps, void* y, uint8_t* q, uint8_t* sf, uint32_t* err,
                       cudaStream_t st);
+// Owner side of the combine fused into the experts' FC2 epilogue: waits for
+// every rank's arrival, then per own token row t: sum over k (ids[t][k] >= 0,
+// in k order) of comb[p][t][k] + add[t] (shared expert, optional) + residual,
+// RMSNorm (+ MXFP8) as b200_ar_reduce_norm.
+int b200_ep_comb_reduce_norm(int T_r, int hidden, int K, const int* ids, const void* add, const ArPeers* peers,
+                             uint32_t* epoch, uint32_t* ticket, float* residual, const float* w, float eps, void* y,
+                             uint8_t* q, uint8_t* sf, uint32_t* err, cudaStream_t st);
+// DeepSeek-V4 sublayer boundary under TP: sum of the pushed partials y (push
+// protocol) fused with the hyper-connection post X <- post y + comb^T X
+// (hc = 4 bf16 streams [T, 4, D], in place) and the row sum of squares.
+int b200_ar_hc_post(int T, int D, const ArPeers* peers, uint32_t* epoch, uint32_t* ticket, int expected, void* X,
+                    const float* post, const float* comb, float* sumsq, uint32_t* err, cudaStream_t st);
 
 // ---------------------------------------------------------------------------
 // Expert-parallel dispatch buffer (symmetric, identical layout on every rank):
@@ -105,9 +126,11 @@ int b200_ep_dispatch(const uint8_t* q, const uint8_t* sf, const float* g, int fp
 // rank's dispatch; bounded).  release = 1 (no ep_gather follows: the expert
 // GEMM reads the received rows in place): also frees the parity (counters to
 // zero, epoch + 1), so the consumer finds the rows at parity (epoch + 1) & 1.
+// row_pair (optional): sorted row -> pair index (token * K + k), for the
+// combine fused into the experts' FC2 epilogue.
 int b200_ep_align(const EpPeers* peers, int T_step, int first, int E, int* seg_start, int* seg_count, int* row_token,
                   float* row_weight, int* pair_row, int* total_rows, int bn1, int* ttile1, int bn2, int* ttile2,
-                  uint32_t* epoch, uint32_t* err, int release, cudaStream_t st);
+                  uint32_t* epoch, uint32_t* err, int release, cudaStream_t st, int* row_pair = nullptr);
 // Gather received rows into the expert-sorted operand; the last CTA frees
 // the parity (counters to zero, epoch + 1).
 int b200_ep_gather(const EpPeers* peers, int T_step, const int* pair_row, int fp4, uint8_t* dq, uint8_t* dsf, float* dg,

@@ -69,6 +69,46 @@ void moe_combine_push(const at::Tensor& y, const at::Tensor& pair_row, c10::opti
 
 int64_t ar_buffer_size(int64_t world, int64_t max_t, int64_t hidden) { return ar_buffer_bytes(world, max_t, hidden); }
 int64_t nvls_buffer_size(int64_t max_t, int64_t hidden) { return nvls_buffer_bytes(max_t, hidden); }
+int64_t ep_ar_buffer_size(int64_t world, int64_t max_t, int64_t hidden, int64_t K) {
+  return ar_buffer_bytes_ep(world, max_t, hidden, K);
+}
+int64_t ep_combine_offset(int64_t world, int64_t max_t, int64_t hidden) { return ep_combine_off(world, max_t, hidden); }
+
+void ep_comb_reduce_norm(int64_t T_r, int64_t hidden, int64_t K, const at::Tensor& ids, c10::optional<at::Tensor> add,
+                         std::vector<int64_t> bases, int64_t rank, int64_t max_t, at::Tensor epoch, at::Tensor ticket,
+                         at::Tensor residual, const at::Tensor& w, double eps, c10::optional<at::Tensor> y,
+                         c10::optional<at::Tensor> q, c10::optional<at::Tensor> sf, at::Tensor err) {
+  TORCH_CHECK(residual.is_cuda() && residual.scalar_type() == at::kFloat && residual.is_contiguous(), "residual fp32");
+  TORCH_CHECK(ids.scalar_type() == at::kInt && ids.is_contiguous() && ids.size(1) == K, "ids int32 [T, K]");
+  if (add.has_value()) TORCH_CHECK(add->scalar_type() == at::kBFloat16 && add->is_contiguous(), "add bf16 [T, H]");
+  const c10::cuda::CUDAGuard g(residual.device());
+  ArPeers p = make_peers(bases, rank, max_t);
+  const int rc = b200_ep_comb_reduce_norm(T_r, hidden, K, ids.data_ptr<int>(), optr<void>(add), &p,
+                                          reinterpret_cast<uint32_t*>(epoch.data_ptr()),
+                                          reinterpret_cast<uint32_t*>(ticket.data_ptr()),
+                                          reinterpret_cast<float*>(residual.data_ptr()),
+                                          reinterpret_cast<const float*>(w.data_ptr()), eps, optr<void>(y),
+                                          optr<uint8_t>(q), optr<uint8_t>(sf),
+                                          reinterpret_cast<uint32_t*>(err.data_ptr()),
+                                          at::cuda::getCurrentCUDAStream().stream());
+  TORCH_CHECK(rc == 0, "ep_comb_reduce_norm failed ", rc);
+}
+
+void ar_hc_post(int64_t T, int64_t D, std::vector<int64_t> bases, int64_t rank, int64_t max_t, at::Tensor epoch,
+                at::Tensor ticket, int64_t expected, at::Tensor X, const at::Tensor& post, const at::Tensor& comb,
+                at::Tensor sumsq, at::Tensor err) {
+  TORCH_CHECK(X.is_cuda() && X.scalar_type() == at::kBFloat16 && X.is_contiguous() && X.dim() == 3 && X.size(1) == 4,
+              "X bf16 [T, 4, D]");
+  TORCH_CHECK(post.scalar_type() == at::kFloat && comb.scalar_type() == at::kFloat && sumsq.scalar_type() == at::kFloat,
+              "post / comb / sumsq fp32");
+  const c10::cuda::CUDAGuard g(X.device());
+  ArPeers p = make_peers(bases, rank, max_t);
+  const int rc = b200_ar_hc_post(T, D, &p, reinterpret_cast<uint32_t*>(epoch.data_ptr()),
+                                 reinterpret_cast<uint32_t*>(ticket.data_ptr()), expected, X.data_ptr(),
+                                 post.data_ptr<float>(), comb.data_ptr<float>(), sumsq.data_ptr<float>(),
+                                 reinterpret_cast<uint32_t*>(err.data_ptr()), at::cuda::getCurrentCUDAStream().stream());
+  TORCH_CHECK(rc == 0, "ar_hc_post failed ", rc);
+}
 
 void nvls_ar_norm(int64_t T, int64_t hidden, std::vector<int64_t> bases, int64_t rank, int64_t max_t, int64_t mc,
                   at::Tensor epoch, at::Tensor ticket, int64_t expected, at::Tensor residual, const at::Tensor& w,
@@ -138,15 +178,18 @@ void ep_dispatch(const at::Tensor& q, const at::Tensor& sf, c10::optional<at::Te
 void ep_align(std::vector<int64_t> bases, int64_t rank, int64_t max_t, int64_t hidden, int64_t K, int64_t T_step,
               int64_t first, int64_t E, at::Tensor seg_start, at::Tensor seg_count, at::Tensor row_token,
               at::Tensor row_weight, at::Tensor pair_row, at::Tensor total_rows, int64_t bn1, at::Tensor ttile1,
-              int64_t bn2, at::Tensor ttile2, const at::Tensor& epoch, at::Tensor err, bool release) {
+              int64_t bn2, at::Tensor ttile2, const at::Tensor& epoch, at::Tensor err, bool release,
+              c10::optional<at::Tensor> row_pair) {
   const c10::cuda::CUDAGuard g(pair_row.device());
   EpPeers p = make_ep(bases, rank, max_t, hidden, K);
   TORCH_CHECK(pair_row.numel() == p.world * T_step * K, "pair_row [world*T_step, K]");
+  if (row_pair.has_value()) TORCH_CHECK(row_pair->numel() >= row_token.numel(), "row_pair as long as row_token");
   const int rc = b200_ep_align(&p, T_step, first, E, seg_start.data_ptr<int>(), seg_count.data_ptr<int>(),
                                row_token.data_ptr<int>(), row_weight.data_ptr<float>(), pair_row.data_ptr<int>(),
                                total_rows.data_ptr<int>(), bn1, ttile1.data_ptr<int>(), bn2, ttile2.data_ptr<int>(),
                                reinterpret_cast<uint32_t*>(epoch.data_ptr()),
-                               reinterpret_cast<uint32_t*>(err.data_ptr()), release ? 1 : 0, cur());
+                               reinterpret_cast<uint32_t*>(err.data_ptr()), release ? 1 : 0, cur(),
+                               optr<int>(row_pair));
   TORCH_CHECK(rc == 0, "ep_align failed ", rc);
 }
 
@@ -231,6 +274,10 @@ void register_comm(pybind11::module& m) {
   m.def("ar_buffer_size", &ar_buffer_size);
   m.def("nvls_buffer_size", &nvls_buffer_size);
   m.def("nvls_ar_norm", &nvls_ar_norm);
+  m.def("ar_hc_post", &ar_hc_post);
+  m.def("ep_ar_buffer_size", &ep_ar_buffer_size);
+  m.def("ep_combine_offset", &ep_combine_offset);
+  m.def("ep_comb_reduce_norm", &ep_comb_reduce_norm);
   m.def("moe_combine_push", &moe_combine_push, pybind11::arg("y"), pybind11::arg("pair_row"), pybind11::arg("add"),
         pybind11::arg("bases"), pybind11::arg("rank"), pybind11::arg("max_t"), pybind11::arg("epoch"),
         pybind11::arg("ticket"), pybind11::arg("nctas"), pybind11::arg("mc") = 0);
@@ -242,7 +289,7 @@ void register_comm(pybind11::module& m) {
         pybind11::arg("seg_start"), pybind11::arg("seg_count"), pybind11::arg("row_token"), pybind11::arg("row_weight"),
         pybind11::arg("pair_row"), pybind11::arg("total_rows"), pybind11::arg("bn1"), pybind11::arg("ttile1"),
         pybind11::arg("bn2"), pybind11::arg("ttile2"), pybind11::arg("epoch"), pybind11::arg("err"),
-        pybind11::arg("release") = false);
+        pybind11::arg("release") = false, pybind11::arg("row_pair") = pybind11::none());
   m.def("ep_gather", &ep_gather);
   m.def("ep_combine_rs", &ep_combine_rs);
   m.def("lm_candidates", &lm_candidates);

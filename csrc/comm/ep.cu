@@ -100,7 +100,8 @@ __global__ void __launch_bounds__(kThreads) ep_dispatch_kernel(const uint8_t* __
 __global__ void __launch_bounds__(1024) ep_align_kernel(EpPeers P, int T_step, int first, int E, int* seg_start,
                                                         int* seg_count, int* row_token, float* row_weight,
                                                         int* pair_row, int* total_rows, int bn1, int* ttile1, int bn2,
-                                                        int* ttile2, uint32_t* epoch, uint32_t* err, int release) {
+                                                        int* ttile2, uint32_t* epoch, uint32_t* err, int release,
+                                                        int* row_pair) {
   extern __shared__ int sh[];
   __shared__ int ok_s;
   pdl_wait();
@@ -116,7 +117,7 @@ __global__ void __launch_bounds__(1024) ep_align_kernel(EpPeers P, int T_step, i
     for (int i = threadIdx.x; i < P.world * T_step * P.K; i += blockDim.x) pair_row[i] = -1;
   moe::moe_align_body(reinterpret_cast<const int*>(reg + P.off_ids), reinterpret_cast<const float*>(reg + P.off_w), T,
                       P.K, first, E, seg_start, seg_count, row_token, row_weight, pair_row, total_rows, bn1, ttile1, bn2,
-                      ttile2, sh);
+                      ttile2, sh, row_pair);
   if (release) {
     // every thread read the epoch above; the rows stay in place for the
     // expert GEMM of this layer, and the next push into parity p comes two
@@ -236,11 +237,11 @@ int b200_ep_dispatch(const uint8_t* q, const uint8_t* sf, const float* g, int fp
 
 int b200_ep_align(const EpPeers* peers, int T_step, int first, int E, int* seg_start, int* seg_count, int* row_token,
                   float* row_weight, int* pair_row, int* total_rows, int bn1, int* ttile1, int bn2, int* ttile2,
-                  uint32_t* epoch, uint32_t* err, int release, cudaStream_t st) {
+                  uint32_t* epoch, uint32_t* err, int release, cudaStream_t st, int* row_pair) {
   if (T_step <= 0 || T_step > peers->max_t) return -1;
   b200::launch_pdl(b200::ep::ep_align_kernel, dim3(1), dim3(1024), 3 * E * sizeof(int), st, *peers, T_step, first, E,
                    seg_start, seg_count, row_token, row_weight, pair_row, total_rows, bn1 > 0 ? bn1 : 128, ttile1,
-                   bn2 > 0 ? bn2 : 128, ttile2, epoch, err, release);
+                   bn2 > 0 ? bn2 : 128, ttile2, epoch, err, release, row_pair);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
 

@@ -73,3 +73,11 @@ int b200_e5_prune(int* ids, float* w, int T, int K, int E, float budget, int max
 // Tracing (see trace.cu): %globaltimer into buf[idx] once the stream's
 // previous kernel has completed.
 int b200_trace_stamp(void* buf, int idx, cudaStream_t st);
+
+// L2 prefetch of up to four regions (16-byte aligned) by `nctas` CTAs.
+struct L2Regions {
+  const void* ptr[4];
+  int64_t bytes[4];
+  int n;
+};
+int b200_l2_prefetch(const L2Regions* r, int nctas, cudaStream_t st);

@@ -24,7 +24,7 @@ __device__ __forceinline__ int64_t sf_offset(int row, int kblock, int kb_total) 
 __device__ __forceinline__ void moe_align_body(const int* ids, const float* w, int T, int K, int first, int E,
                                                int* seg_start, int* seg_count, int* row_token, float* row_weight,
                                                int* pair_row, int* total_rows, int bn1, int* ttile1, int bn2,
-                                               int* ttile2, int* sh) {
+                                               int* ttile2, int* sh, int* row_pair = nullptr) {
   int* cnt = sh;          // [E]
   int* start = sh + E;    // [E]
   int* fill = sh + 2 * E; // [E]
@@ -62,6 +62,7 @@ __device__ __forceinline__ void moe_align_body(const int* ids, const float* w, i
       row_token[r] = i / K;
       row_weight[r] = __ldcg(w + i);
       pair_row[i] = r;
+      if (row_pair) row_pair[r] = i;
     } else {
       pair_row[i] = -1;
     }

@@ -36,6 +36,7 @@
 #include <cuda_fp8.h>
 
 #include "../common/ptx.cuh"
+#include "../comm/comm_dev.cuh"
 #include "elementwise.h"
 #include "row_util.cuh"
 
@@ -93,6 +94,86 @@ __global__ void __launch_bounds__(kThreads) hc_post_kernel(__nv_bfloat16* X, con
   }
   ss = block_sum(ss, red);
   if (threadIdx.x == 0) sumsq[t] = ss;
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-parallel all-reduce fused with hc_post (the sublayer boundary of the
+// V4 family under TP): every rank pushed its partial sublayer output y into
+// recv[p][rank] of every rank (P2P stores by ar_push or the o-projection's
+// GEMM epilogue, one arrival per source); each CTA waits (bounded) for the
+// arrivals, sums the world partials in rank order (fp32, rounded to bf16 like
+// the unfused all-reduce's output) and applies hc_post to its row.  The last
+// CTA (ticket) zeroes the parity's counters and advances the epoch, as the
+// push reduction does.  Replaces NCCL all-reduce + hc_post (two launches and
+// a global round trip of y); fin.py:1-20 fuses the same boundary on TP2.
+__global__ void __launch_bounds__(kThreads) ar_hc_post_kernel(int D, ArPeers peers, uint32_t* epoch,
+                                                              uint32_t* ticket, uint32_t expected,
+                                                              __nv_bfloat16* X, const float* post, const float* comb,
+                                                              float* sumsq, uint32_t* err) {
+  __shared__ float red[32];
+  __shared__ float cf[kHC * kHC + kHC];
+  __shared__ int ok_s;
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  const int p = (*epoch) & 1;
+  uint8_t* mine = peers.base[peers.rank];
+  const bool ok = comm::wait_arrivals(mine, p, peers.world, expected, err, &ok_s);
+  const int t = blockIdx.x;
+  if (threadIdx.x < kHC * kHC) cf[threadIdx.x] = __ldcg(comb + (int64_t)t * kHC * kHC + threadIdx.x);
+  if (threadIdx.x < kHC) cf[kHC * kHC + threadIdx.x] = __ldcg(post + (int64_t)t * kHC + threadIdx.x);
+  __syncthreads();
+  float ss = 0.f;
+  if (ok) {
+    __nv_bfloat16* xt = X + (int64_t)t * kHC * D;
+    const __nv_bfloat16* y0 = comm::recv_slot(mine, p, 0, peers.world, peers.max_t, D) + (int64_t)t * D;
+    const int64_t sstride = (int64_t)peers.max_t * D;
+    for (int v = threadIdx.x * 8; v < D; v += kThreads * 8) {
+      float yv[8], xr[kHC][8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) yv[i] = 0.f;
+      for (int src = 0; src < peers.world; ++src) {
+        const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(y0 + src * sstride + v));
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __bfloat1622float2(h[i]);
+          yv[2 * i] += f.x;
+          yv[2 * i + 1] += f.y;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) yv[i] = bf16_round(yv[i]);
+#pragma unroll
+      for (int r = 0; r < kHC; ++r) load8(xt + (int64_t)r * D + v, xr[r]);
+#pragma unroll
+      for (int c = 0; c < kHC; ++c) {
+        float o[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float a = cf[kHC * kHC + c] * yv[i];
+#pragma unroll
+          for (int r = 0; r < kHC; ++r) a = fmaf(cf[r * kHC + c], xr[r][i], a);
+          o[i] = bf16_round(a);
+          ss = fmaf(o[i], o[i], ss);
+        }
+        store8_bf16(xt + (int64_t)c * D + v, o);
+      }
+    }
+  }
+  ss = block_sum(ss, red);
+  if (threadIdx.x == 0) sumsq[t] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t k = atomicAdd(ticket, 1u);
+    if (k == gridDim.x - 1) {
+      uint32_t* cnt = comm::counters(mine, p);
+      for (int src = 0; src < peers.world; ++src) atomicExch(cnt + src, 0u);
+      *ticket = 0u;
+      __threadfence();
+      atomicAdd(epoch, 1u);
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -564,6 +645,15 @@ int b200_hc_post(void* X, const void* y, int64_t ldy, const float* post, const f
   if (hc != kHC || D % 8 || ldy % 8) return -1;
   b200::launch_pdl(hc_post_kernel, dim3(T), dim3(kThreads), 0, st, reinterpret_cast<__nv_bfloat16*>(X),
                    reinterpret_cast<const __nv_bfloat16*>(y), ldy, post, comb, D, sumsq);
+  return cudaGetLastError() == cudaSuccess ? 0 : 1;
+}
+
+int b200_ar_hc_post(int T, int D, const ArPeers* peers, uint32_t* epoch, uint32_t* ticket, int expected, void* X,
+                    const float* post, const float* comb, float* sumsq, uint32_t* err, cudaStream_t st) {
+  if (T <= 0) return 0;
+  if (D % 8 || T > peers->max_t || peers->mc || expected <= 0) return -1;
+  b200::launch_pdl(b200::v4::ar_hc_post_kernel, dim3(T), dim3(b200::v4::kThreads), 0, st, D, *peers, epoch, ticket,
+                   (uint32_t)expected, reinterpret_cast<__nv_bfloat16*>(X), post, comb, sumsq, err);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
 

@@ -17,6 +17,22 @@ T* optr(const c10::optional<at::Tensor>& t) {
 
 void chk(int rc, const char* what) { TORCH_CHECK(rc == 0, what, " failed (", rc, ")"); }
 
+// L2 prefetch of the given tensors' bytes (each at most the first `limit`
+// bytes; 16-byte aligned starts) on the current stream.
+void l2_prefetch(std::vector<at::Tensor> ts, int64_t limit, int64_t nctas) {
+  TORCH_CHECK(ts.size() <= 4, "at most 4 regions");
+  L2Regions r{};
+  for (auto& t : ts) {
+    TORCH_CHECK(t.is_cuda() && t.is_contiguous(), "contiguous CUDA tensors");
+    r.ptr[r.n] = t.data_ptr();
+    r.bytes[r.n] = std::min<int64_t>(t.numel() * t.element_size(), limit);
+    ++r.n;
+  }
+  if (r.n == 0) return;
+  const c10::cuda::CUDAGuard g(ts[0].device());
+  chk(b200_l2_prefetch(&r, nctas, at::cuda::getCurrentCUDAStream().stream()), "l2_prefetch");
+}
+
 void hc_post(at::Tensor X, const at::Tensor& y, const at::Tensor& post, const at::Tensor& comb, at::Tensor sumsq) {
   TORCH_CHECK(X.is_cuda() && X.dim() == 3 && X.is_contiguous() && X.scalar_type() == at::kBFloat16, "X bf16 [T,hc,D]");
   TORCH_CHECK(y.scalar_type() == at::kBFloat16 && y.stride(1) == 1, "y bf16 [T, D]");
@@ -167,6 +183,7 @@ void trace_stamp(at::Tensor buf, int64_t idx) {
 void register_v4(pybind11::module& m) {
   m.def("trace_stamp", &trace_stamp);
   m.def("hc_post", &hc_post);
+  m.def("l2_prefetch", &l2_prefetch);
   m.def("hc_pre", &hc_pre);
   m.def("hc_mean", &hc_mean);
   m.def("hc_embed", &hc_embed);

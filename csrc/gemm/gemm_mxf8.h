@@ -136,6 +136,17 @@ struct MoeFusedArgs {
   const uint32_t* src_epoch;
   int src_epoch_add;
   int64_t src_par_bytes;
+  // expert-parallel combine in the FC2 epilogue (c_row_pair set): the
+  // weighted output row of pair (token, k) is stored straight into the
+  // token's owner rank (P2P), slot [parity][token's row there][k] of that
+  // rank's combine region, instead of into y; the last CTA then publishes one
+  // arrival on every rank.  Token = src rank * c_T_step + its row there.
+  const int* c_row_pair;     // sorted row -> pair index token * c_K + k
+  int c_K, c_T_step;
+  uint8_t* c_base[8];
+  int c_rank, c_world, c_max_t;
+  int64_t c_off;             // bytes from a rank's symmetric base to its combine region
+  const uint32_t* c_epoch;   // parity = *c_epoch & 1
 };
 int b200_moe_fused(const MoeFusedArgs* args, cudaStream_t stream);
 

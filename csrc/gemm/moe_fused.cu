@@ -24,6 +24,7 @@
 // the counters, so the launch is graph-replayable.  All waits are bounded.
 #include "../common/ptx.cuh"
 #include "gemm_mxf8.h"
+#include "../comm/comm.h"
 
 namespace b200 {
 namespace moef {
@@ -88,6 +89,13 @@ struct Params {
   const uint32_t* src_epoch;
   int src_epoch_add;
   int64_t src_par_bytes;
+  // expert-parallel combine in the FC2 epilogue (MoeFusedArgs)
+  const int* c_row_pair;
+  int c_K, c_T_step;
+  uint8_t* c_base[8];
+  int c_rank, c_world, c_max_t;
+  int64_t c_off;
+  const uint32_t* c_epoch;
 };
 
 __device__ __forceinline__ int64_t sf_offset(int row, int kblock, int kb_total) {
@@ -504,6 +512,7 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap tm_w1, const __grid_constan
         }
       } else {
         const float wg = FP4 ? __ldcg(p.w2_g + d.e) * p.out_g : 1.f;
+        const int cpar = p.c_row_pair ? int(__ldcg(p.c_epoch) & 1u) : 0;
 #pragma unroll 1
         for (int a = 0; a < 2; ++a) {
           const int wrow = d.n * 2 * kTileM + a * kTileM + sub * 32 + lane;   // hidden row
@@ -517,7 +526,19 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap tm_w1, const __grid_constan
               if (c0 + j < tmax) {
                 const int orow = b_row + c0 + j;
                 const float v = __uint_as_float(r[j]) * __ldcg(p.row_weight + orow) * wg;
-                p.y[(int64_t)orow * p.ldy + wrow] = __float2bfloat16(v);
+                if (p.c_row_pair) {
+                  // pair (token, k) -> its owner's combine slot [parity][row there][k] (P2P store)
+                  const int pair = __ldcg(p.c_row_pair + orow);
+                  const int tok = pair / p.c_K;
+                  const int kk = pair - tok * p.c_K;
+                  const int dst = tok / p.c_T_step;
+                  const int tl = tok - dst * p.c_T_step;
+                  __nv_bfloat16* slot = reinterpret_cast<__nv_bfloat16*>(p.c_base[dst] + p.c_off) +
+                                        (((int64_t)cpar * p.c_max_t + tl) * p.c_K + kk) * p.hidden;
+                  slot[wrow] = __float2bfloat16(v);
+                } else {
+                  p.y[(int64_t)orow * p.ldy + wrow] = __float2bfloat16(v);
+                }
               }
             }
           }
@@ -543,15 +564,26 @@ moe_fused_kernel(const __grid_constant__ CUtensorMap tm_w1, const __grid_constan
     tc_fence_after();
     tmem_dealloc(tmem, C::kTmemCols);
   }
-  // the last CTA resets the work counters (graph replays start from zero)
+  // the last CTA resets the work counters (graph replays start from zero);
+  // with the combine fused in, it also publishes this rank's arrival on every
+  // rank (each CTA's system-scope fence orders its peer stores first)
   if (threadIdx.x == 0) {
-    __threadfence();
+    if (p.c_row_pair) __threadfence_system();
+    else __threadfence();
     const int prev = atomicAdd(p.work + 1, 1);
     if (prev == gridDim.x - 1) {
       for (int e = 0; e < E; ++e) p.fc1_done[e] = 0;
       p.work[0] = 0;
       __threadfence();
       p.work[1] = 0;
+      if (p.c_row_pair) {
+        __threadfence_system();
+        const int par = int(__ldcg(p.c_epoch) & 1u);
+        for (int q = 0; q < p.c_world; ++q)
+          asm volatile("red.release.sys.global.add.u32 [%0], %1;"
+                       ::"l"(reinterpret_cast<uint32_t*>(p.c_base[q]) + par * kArMaxRanks + p.c_rank), "r"(1u)
+                       : "memory");
+      }
     }
   }
 }
@@ -639,6 +671,15 @@ static int launch(const MoeFusedArgs& a, cudaStream_t st) {
   }
   p.src_rows = a.src_rows;
   p.row_token = a.row_token;
+  p.c_row_pair = a.c_row_pair;
+  p.c_K = a.c_K;
+  p.c_T_step = a.c_T_step;
+  for (int i = 0; i < 8; ++i) p.c_base[i] = a.c_base[i];
+  p.c_rank = a.c_rank;
+  p.c_world = a.c_world;
+  p.c_max_t = a.c_max_t;
+  p.c_off = a.c_off;
+  p.c_epoch = a.c_epoch;
   p.src_epoch = a.src_epoch;
   p.src_epoch_add = a.src_epoch_add;
   p.src_par_bytes = a.src_par_bytes;
@@ -676,6 +717,9 @@ int b200_moe_fused(const MoeFusedArgs* a, cudaStream_t st) {
       !a->fc1_done)
     return -1;
   if (a->pull && (a->src_rows <= 0 || !a->row_token || !a->src_q[0] || !a->src_sf[0])) return -1;
+  if (a->c_row_pair && (a->c_K <= 0 || a->c_T_step <= 0 || a->c_world < 1 || a->c_world > 8 || !a->c_epoch ||
+                        a->c_T_step > a->c_max_t))
+    return -1;
   if (a->fp4) {
     if (a->hidden % 256 || a->inter % 256 || !a->w1_g || !a->w2_g || (!a->x_g && !a->pull) ||
         (a->pull && !a->src_g[0]) || a->out_g <= 0.f)

@@ -693,3 +693,26 @@ def test_router_gemm_split_k(T):
                    splits=16)
     exp = x.float() @ g.float().T
     assert rel_err(out, exp) < 1e-3
+
+
+def test_l2_prefetch_runs_and_captures():
+    """The L2 prefetch kernel issues bulk prefetches over up to four regions
+    (a hint: no data changes), also inside a captured graph; misaligned
+    starts are refused."""
+    from b200ds import _C
+    a = torch.randint(0, 255, (8 << 20,), dtype=torch.uint8, device=DEV)
+    b = torch.randn(1 << 20, device=DEV)
+    ca, cb = a.clone(), b.clone()
+    _C.l2_prefetch([a, b], 4 << 20, 16)
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            _C.l2_prefetch([a], 1 << 30, 32)
+    torch.cuda.current_stream().wait_stream(s)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(a, ca) and torch.equal(b, cb)
+    with pytest.raises(RuntimeError):
+        _C.l2_prefetch([a[1:]], 1024, 1)

@@ -180,3 +180,52 @@ def test_dp2_ep2_matches_single_gpu(comm_impl, fmt):
     res = run_ranks(_dp_rank, 2, comm_impl, fmt, timeout=600)
     for rank, out, ref in res:
         assert _rel(out, ref) < 0.15, (rank, _rel(out, ref))
+
+
+def _v4_rank(rank, world):
+    import torch
+    import torch.distributed as dist
+    from b200ds import ops
+    from b200ds.config import EngineConfig, small_v4_gpu_config
+    from b200ds.models.batch import build_batch
+    from b200ds.models.loader import build_model
+    from b200ds.models.reference_v4 import init_weights_v4
+    from b200ds.parallel.state import init_parallel
+    ps = init_parallel(backend="nccl", timeout_s=60)
+    ops.set_impl("native")
+    cfg = small_v4_gpu_config()
+    sd = init_weights_v4(cfg, 0)
+    m = build_model(cfg, EngineConfig(tp_size=world, ep_size=world, comm_impl="fused"), ps, sd, device=ps.device)
+    m.allocate_kv(8)
+    g = torch.Generator().manual_seed(5)
+    toks = torch.randint(0, cfg.vocab_size, (40,), generator=g).tolist()
+    seqs = [{"tokens": toks[:17], "start": 0, "pages": [1]}, {"tokens": toks[17:], "start": 0, "pages": [2]}]
+    try:
+        out = m.forward(build_batch(seqs, 64, device=ps.device)).float().cpu()
+    finally:
+        torch.cuda.synchronize()
+        dist.barrier(group=ps.cpu_group)
+    assert ps.fused_ar is not None and ps.fused_ar.nvls is None
+    ps.fused_ar.check()
+    return out
+
+
+def test_v4_tp2_fused_boundary_matches_oracle():
+    """DeepSeek-V4-family model at TP2: every sublayer's all-reduce runs fused
+    with the hyper-connection post (ar_push / GEMM push + ar_hc_post); both
+    ranks agree exactly and follow the fp32 oracle like one GPU does."""
+    _needs(2)
+    from b200ds.config import small_v4_gpu_config
+    from b200ds.models.reference_v4 import ReferenceV4Model, init_weights_v4
+    res = run_ranks(_v4_rank, 2, timeout=600)
+    assert torch.equal(res[0], res[1])
+    cfg = small_v4_gpu_config()
+    oracle = ReferenceV4Model(cfg, init_weights_v4(cfg, 0), 128)
+    g = torch.Generator().manual_seed(5)
+    toks = torch.randint(0, cfg.vocab_size, (40,), generator=g)
+    want = []
+    for seq in (toks[:17], toks[17:]):
+        oracle.reset(1)
+        want.append(oracle.forward(seq.view(1, -1), 0, decode=False)[0, -1])
+    want = torch.stack(want)
+    assert _rel(res[0], want) < 0.15, _rel(res[0], want)
