@@ -217,3 +217,27 @@ def mla_prefill_torch(q_abs: torch.Tensor, q_pe: torch.Tensor, cache: torch.Tens
             p = torch.softmax(s, -1).to(torch.bfloat16)
             out[r0:r1, h0:h0 + head_chunk] = torch.matmul(p, kv[:, :L]).transpose(0, 1)
     return out
+
+
+def prebuild_flashinfer(workspace: str) -> None:
+    """Compile the FlashInfer JIT modules the comparison arm uses (trtllm-gen
+    fused MoE and MLA decode launchers) for sm_100a into `workspace` (the
+    FLASHINFER_WORKSPACE_BASE the bench's baseline arm points at).  Runs on a
+    machine without a GPU; the kernels themselves come from FlashInfer's
+    packaged cubins."""
+    import os
+    os.environ["FLASHINFER_WORKSPACE_BASE"] = workspace
+    os.environ.setdefault("FLASHINFER_CUDA_ARCH_LIST", "10.0a")
+    from flashinfer.jit.attention.modules import gen_trtllm_gen_fmha_module
+    from flashinfer.fused_moe.core import gen_trtllm_gen_fused_moe_sm100_module
+    for spec in (gen_trtllm_gen_fused_moe_sm100_module(), gen_trtllm_gen_fmha_module()):
+        spec.build(verbose=False)        # compile only (loading needs the driver)
+
+
+if __name__ == "__main__":
+    # python -m b200ds.ops.baseline prebuild [workspace]
+    import os
+    import sys
+    if len(sys.argv) > 1 and sys.argv[1] == "prebuild":
+        root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+        prebuild_flashinfer(sys.argv[2] if len(sys.argv) > 2 else os.path.join(root, "baseline", "_fi"))

@@ -345,8 +345,20 @@ def moe_tile_n(rows_per_expert: float, cap: int) -> int:
     return tactics.pick("moe_tile", bn, cap=cap, rows_per_expert=rows_per_expert)
 
 
+def moe_tiles(rows_per_expert: float):
+    """(FC1, FC2) token tiles of the grouped GEMMs.  Decode-sized experts
+    take the smallest tile that holds their rows (weight streaming); from 128
+    rows per expert FC1 runs 128-token tiles (gate + up into one TMEM
+    accumulator) and from 256 rows FC2 runs 256-token tiles, which halve the
+    shared-memory traffic per MMA of the compute-bound prefill GEMMs."""
+    bn1 = 128 if rows_per_expert >= 128 else moe_tile_n(rows_per_expert, 64)
+    bn2 = 256 if rows_per_expert >= 256 else moe_tile_n(rows_per_expert, 128)
+    return (tactics.pick("moe_tile_fc1", bn1, rows_per_expert=rows_per_expert),
+            tactics.pick("moe_tile_fc2", bn2, rows_per_expert=rows_per_expert))
+
+
 def _fused(bn1: int, bn2: int) -> bool:
-    return levers.on("moe_fused") and bn1 == bn2
+    return levers.on("moe_fused") and bn1 == bn2 and bn1 <= 64
 
 
 def _pulls(bn1: int, bn2: int) -> bool:
@@ -427,8 +439,7 @@ def moe_experts(h, w: torch.Tensor, ids: torch.Tensor, ex, out_dtype=torch.bfloa
     I = ex.inter
     e_tot = n_experts_total or E
     exp_rows = T * K / e_tot
-    bn1 = moe_tile_n(exp_rows, 64)
-    bn2 = moe_tile_n(exp_rows, 128)
+    bn1, bn2 = moe_tiles(exp_rows)
     max_rows = round_up(T * K, 128) + E * 128   # 128-aligned segments
     seg_start = torch.empty(E, dtype=torch.int32, device=dev)
     seg_count = torch.empty(E, dtype=torch.int32, device=dev)
@@ -488,8 +499,7 @@ def moe_experts_nvfp4(h, w, ids, ex, out_dtype=torch.bfloat16, n_experts_total=N
     I = ex.inter
     e_tot = n_experts_total or E
     exp_rows = T * K / e_tot
-    bn1 = moe_tile_n(exp_rows, 64)
-    bn2 = moe_tile_n(exp_rows, 128)
+    bn1, bn2 = moe_tiles(exp_rows)
     max_rows = round_up(T * K, 128) + E * 128
     xq, xsf, xg = nvfp4_quant(x)
     seg_start = torch.empty(E, dtype=torch.int32, device=dev)
@@ -550,8 +560,7 @@ def moe_experts_ep(h, w, ids, ex, T_step: int, n_experts_total: int, ep, far=Non
     I = ex.inter
     Tg = ep.world * T_step
     exp_rows = Tg * K / n_experts_total
-    bn1 = moe_tile_n(exp_rows, 64)
-    bn2 = moe_tile_n(exp_rows, 128)
+    bn1, bn2 = moe_tiles(exp_rows)
     max_rows = round_up(Tg * K, 128) + E * 128
     ids = (ids if ids.dtype == torch.int32 else ids.int()).contiguous()
     _C.ep_dispatch(q, sf, g, Hd, ids, w.float().contiguous(), T_step, n_experts_total // ep.world, ep.bases,

@@ -166,6 +166,10 @@ def main():
                           "pyproject; needs cacheon/dsv41-tp2-upstream, FlashInfer 0.7.1, DeepGEMM, sm_103); "
                           "pip install of the reference source tree fails: 'Directory is not installable'"}))
         return
+    if args.impl == "baseline":
+        # FlashInfer's JIT modules of the library arm, prebuilt in-tree (compiling
+        # them on a fresh box takes tens of minutes)
+        os.environ.setdefault("FLASHINFER_WORKSPACE_BASE", os.path.join(ROOT, "baseline", "_fi"))
     import torch
     import torch.distributed as dist
     from b200ds import ops

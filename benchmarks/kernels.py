@@ -112,7 +112,7 @@ def run_moe(fmt: str, T: int, E_total: int, E_local: int, iters: int, h=7168, I=
     dev = torch.device("cuda")
     K = 8
     exp_rows = T * K / E_total
-    bn1, bn2 = cuda.moe_tile_n(exp_rows, 64), cuda.moe_tile_n(exp_rows, 128)
+    bn1, bn2 = cuda.moe_tiles(exp_rows)
     L = _moe_layout(T, K, E_total, E_local, dev, bn1, bn2)
     mr = L["max_rows"]
     sd = _Seeder(3)
@@ -436,6 +436,11 @@ def main():
         ("gemm_o_proj_T512", lambda: run_gemm("o_proj_T512", 512, 7168, 2048, a.iters)),
         ("moe_mxfp8_T2048_ep1", lambda: run_moe("mxfp8", 512 if small else 2048, 256, 64 if small else 256,
                                                  a.iters)),
+        # a 16K-token prefill chunk: ~512 rows per expert, 128 / 256-token tiles
+        ("moe_mxfp8_T16384_ep1", lambda: run_moe("mxfp8", 2048 if small else 16384, 256, 32 if small else 256,
+                                                  a.iters)),
+        ("moe_nvfp4_T16384_ep1", lambda: run_moe("nvfp4", 2048 if small else 16384, 256, 32 if small else 256,
+                                                  a.iters)),
         ("v4_T64", lambda: run_v4(64, a.iters)),
     ]
     for name, fn in cases:

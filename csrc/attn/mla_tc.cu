@@ -28,11 +28,10 @@
 //
 // Sparse variant (SPARSE = true): the query attends only to the cache
 // positions in its top-k list (-1 = unused entry).  The KV rows of a tile are
-// then scattered over pages, so the whole producer warp gathers them with
-// 16-byte cp.async copies written in the same 128B / 64B swizzled layout the
-// TMA boxes would produce (the MMA descriptors are shared with the dense
-// path); a proxy fence makes the copies visible to the tensor cores before
-// the stage's barrier is signalled.
+// then scattered over pages; TMA tile::gather4 loads (this GPU's cache, no
+// multicast) bring four rows per instruction into the same 128B / 64B
+// swizzled layout the dense boxes produce, so the MMA descriptors are shared
+// with the dense path and the stage completes on its transaction bytes.
 //
 // Reference parity: the reference's own sparse-MLA decode kernel `bsx`
 // (ro_unit.cu:480; c36s SPA design ro_unit.cu:136-172) uses the same
@@ -175,7 +174,7 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], SPARSE ? 32 : 1);
+      mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], kSmThreads / 32);    // one arrival per softmax warp
@@ -199,6 +198,14 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
   if (warp == 0) {
     // ------------------------------ producer ------------------------------
     if (SPARSE && nt > 0) {
+      // Sparse rows are gathered by TMA (tile::gather4: four cache rows of one
+      // 128-byte latent column box, or of the 64-byte rope box, per
+      // instruction, into the same swizzled layout the dense boxes produce).
+      // Lane l resolves rows 4l..4l+3 of the tile to cache rows and issues
+      // their five gathers; lane 0 posts the stage's byte count first.  Rows
+      // with no entry read the sequence's position 0 (always written) and are
+      // masked to -inf by the softmax.  Completion is tracked by the stage's
+      // transaction bytes, so the producer never waits for its own copies.
       if (lane == 0) {
         const int qrow = t * p.H + h0;
         mbar_arrive_expect_tx(q_full, S::kQLat + S::kQRope);
@@ -207,32 +214,27 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
       }
       __syncwarp();
       const int* list = p.topk + (int64_t)t * p.topk_n;
+      const int64_t row0 = (int64_t)__ldcg(p.block_table + (int64_t)b * p.bt_stride) * kPage;   // position 0
       for (int i = 0; i < nt; ++i) {
         const int s = i % kStages;
         if (i >= kStages && !mbar_wait(&kv_empty[s], ((i / kStages) - 1) & 1, p.err)) break;
-        const uint32_t dst = smem_u32(sKV + s * S::kKVStage);
+        uint8_t* dst = sKV + s * S::kKVStage;
         const int tok0 = k_lo + i * kTile;
-#pragma unroll 1
-        for (int q = 0; q < kTile / 32; ++q) {
-          const int r = q * 32 + lane;                       // row of the tile
-          const int j = tok0 + r;                            // list entry
+        if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], S::kKVStage);
+        __syncwarp();
+        int rows[4];
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const int j = tok0 + 4 * lane + m;                 // list entry of tile row 4 lane + m
           const int pos = j < k_hi ? __ldcg(list + j) : -1;
-          const bool ok = pos >= 0 && pos < n;
-          int64_t slot = 0;
-          if (ok) slot = (int64_t)__ldcg(p.block_table + (int64_t)b * p.bt_stride + pos / kPage) * kPage + pos % kPage;
-          const uint8_t* src = p.cache + slot * kD;
-          const uint32_t nb = ok ? 16u : 0u;
-#pragma unroll
-          for (int c = 0; c < 32; ++c)                       // latent: 4 boxes of 128 B, 128B swizzle
-            cp_async_16(dst + (c >> 3) * kTile * 128 + r * 128 + (((c & 7) ^ (r & 7)) << 4), src + c * 16, nb);
-#pragma unroll
-          for (int c = 0; c < 4; ++c)                        // rope: 64 B rows, 64B swizzle
-            cp_async_16(dst + S::kKVLat + r * 64 + ((c ^ ((r >> 1) & 3)) << 4), src + kL + c * 16, nb);
+          rows[m] = (pos >= 0 && pos < n)
+                        ? __ldcg(p.block_table + (int64_t)b * p.bt_stride + pos / kPage) * kPage + pos % kPage
+                        : int(row0);
         }
-        cp_async_commit();
-        cp_async_wait_all();
-        fence_proxy_async_smem();
-        mbar_arrive(&kv_full[s]);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)                          // latent: 4 boxes of 128 B
+          tma_gather4(dst + c * kTile * 128 + 4 * lane * 128, &tm_kv_lat, &kv_full[s], c * 128, rows);
+        tma_gather4(dst + S::kKVLat + 4 * lane * 64, &tm_kv_rope, &kv_full[s], kL, rows);
       }
     } else if (!SPARSE && lane == 0 && nt > 0) {
       const int qrow = t * p.H + h0;
@@ -635,8 +637,10 @@ static int launch(const MlaTcArgs& a, cudaStream_t st) {
   const int64_t qrows = (int64_t)a.T * a.H;
   if (map2d(&mql, a.q8, qrows, HB, 128, CU_TENSOR_MAP_SWIZZLE_128B)) return -2;
   if (map2d(&mqr, a.q8, qrows, HB, 64, CU_TENSOR_MAP_SWIZZLE_64B)) return -3;
-  if (map2d(&mkl, a.cache, a.cache_rows, kPage, 128, CU_TENSOR_MAP_SWIZZLE_128B)) return -4;
-  if (map2d(&mkr, a.cache, a.cache_rows, kPage, 64, CU_TENSOR_MAP_SWIZZLE_64B)) return -5;
+  // dense: one 64-row page per box; sparse: one-row boxes for tile::gather4
+  const int kv_box_rows = SPARSE ? 1 : kPage;
+  if (map2d(&mkl, a.cache, a.cache_rows, kv_box_rows, 128, CU_TENSOR_MAP_SWIZZLE_128B)) return -4;
+  if (map2d(&mkr, a.cache, a.cache_rows, kv_box_rows, 64, CU_TENSOR_MAP_SWIZZLE_64B)) return -5;
   Params p{};
   p.block_table = a.block_table;
   p.bt_stride = a.bt_stride;

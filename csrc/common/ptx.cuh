@@ -128,6 +128,19 @@ B200_DEVICE void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* b
       : "memory");
 }
 
+// TMA gather of four rows (rows[0..3]) of one column box starting at byte
+// column x of a 2-D tensor map whose box is one row high (this GPU's memory;
+// no cluster broadcast).  The rows land consecutively at smem_dst, swizzled
+// by the map's mode like a 4-row box.
+B200_DEVICE void tma_gather4(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int32_t x, const int (&rows)[4]) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];"
+      ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(rows[0]),
+        "r"(rows[1]), "r"(rows[2]), "r"(rows[3])
+      : "memory");
+}
+
 // 1-D bulk copy: both addresses 16-byte aligned, bytes a multiple of 16.
 B200_DEVICE void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
   asm volatile(

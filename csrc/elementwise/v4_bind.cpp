@@ -24,6 +24,7 @@ void l2_prefetch(std::vector<at::Tensor> ts, int64_t limit, int64_t nctas) {
   L2Regions r{};
   for (auto& t : ts) {
     TORCH_CHECK(t.is_cuda() && t.is_contiguous(), "contiguous CUDA tensors");
+    TORCH_CHECK((reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0, "regions must start on 16 bytes");
     r.ptr[r.n] = t.data_ptr();
     r.bytes[r.n] = std::min<int64_t>(t.numel() * t.element_size(), limit);
     ++r.n;

@@ -43,15 +43,19 @@ struct Cfg {
   static constexpr int kStageBytes = kLoadBytes + kSfK;   // + padding after the activation scale chunks
   static constexpr int kAcc = kA * BN;                      // columns per accumulator buffer
   static constexpr int kSlotCols = FP4 ? 16 * kA + 16 : 4 * kA + 4;   // scale columns per stage
+  // Two accumulator buffers (the epilogue drains one while the MMAs fill the
+  // other) when they leave TMEM room for four scale slots; the wide prefill
+  // tiles (FC1 gate + up at 128 tokens, FC2 at 256) keep one.
+  static constexpr int kBufs = (2 * kAcc + 4 * kSlotCols <= 512) ? 2 : 1;
   // Stages bounded by shared memory and by TMEM (one scale slot per stage, so
   // a slot is rewritten only after its stage's MMAs released the stage).
-  static constexpr int kStagesSmem = (200 * 1024) / kStageBytes;
-  static constexpr int kStagesTmem = (512 - 2 * kAcc) / kSlotCols;
+  static constexpr int kStagesSmem = (208 * 1024) / kStageBytes;
+  static constexpr int kStagesTmem = (512 - kBufs * kAcc) / kSlotCols;
   static constexpr int kStages0 = kStagesSmem < kStagesTmem ? kStagesSmem : kStagesTmem;
   static constexpr int kStages = kStages0 > 16 ? 16 : kStages0;
   static constexpr int kSfSlots = kStages;
   static constexpr int kSfCols = kSfSlots * kSlotCols;
-  static constexpr int kNeed = 2 * kAcc + kSfCols;
+  static constexpr int kNeed = kBufs * kAcc + kSfCols;
   static constexpr int kTmemCols = kNeed <= 32 ? 32 : kNeed <= 64 ? 64 : kNeed <= 128 ? 128 : kNeed <= 256 ? 256 : 512;
   static_assert(kNeed <= 512, "TMEM budget");
   static_assert(kStages >= 2, "pipeline depth");
@@ -157,7 +161,7 @@ grouped_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  const uint32_t tmem_sf = tmem + 2 * C::kAcc;
+  const uint32_t tmem_sf = tmem + C::kBufs * C::kAcc;
 
   pdl_wait();
   if (threadIdx.x == 0) pdl_launch_dependents();   // dependents wait for this grid's completion
@@ -224,8 +228,8 @@ grouped_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
     for (int w = blockIdx.x; ok && w < total; w += gridDim.x, ++c) {
       const Tile t = map_tile(p, lay, w);
       const int b_row = lay[p.E + 1 + t.e] + t.tt * BN;
-      const int buf = c & 1;
-      if (c >= 2 && !mbar_wait(&acc_empty[buf], ((c >> 1) - 1) & 1, p.err)) { ok = false; break; }
+      const int buf = c % C::kBufs;
+      if (c >= C::kBufs && !mbar_wait(&acc_empty[buf], ((c / C::kBufs) - 1) & 1, p.err)) { ok = false; break; }
       tc_fence_after();
       const uint32_t acc = tmem + buf * C::kAcc;
       for (int kt = 0; kt < nk; ++kt, ++it) {
@@ -292,8 +296,8 @@ grouped_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
     const int kb_out = p.ldq / 32;
     for (int w = blockIdx.x; w < total; w += gridDim.x, ++c) {
       const Tile t = map_tile(p, lay, w);
-      const int buf = c & 1;
-      if (!mbar_wait(&acc_full[buf], (c >> 1) & 1, p.err)) break;
+      const int buf = c % C::kBufs;
+      if (!mbar_wait(&acc_full[buf], (c / C::kBufs) & 1, p.err)) break;
       tc_fence_after();
       const int b_row = lay[p.E + 1 + t.e] + t.tt * BN;
       const int tmax = t.rows - t.tt * BN;
@@ -480,8 +484,9 @@ static int launch_bn(const GroupedArgs& a, cudaStream_t st) {
     case 16: return launch<16, EPI, FP4>(a, st);
     case 32: return launch<32, EPI, FP4>(a, st);
     case 64: return launch<64, EPI, FP4>(a, st);
-    case 128:
-      if constexpr (EPI != kEpiSwiglu) return launch<128, EPI, FP4>(a, st);
+    case 128: return launch<128, EPI, FP4>(a, st);
+    case 256:
+      if constexpr (EPI != kEpiSwiglu) return launch<256, EPI, FP4>(a, st);
       return -4;
   }
   return -4;

@@ -716,3 +716,36 @@ def test_l2_prefetch_runs_and_captures():
     assert torch.equal(a, ca) and torch.equal(b, cb)
     with pytest.raises(RuntimeError):
         _C.l2_prefetch([a[1:]], 1024, 1)
+
+
+@pytest.mark.parametrize("fp4", [False, True])
+def test_moe_experts_prefill_tiles(fp4):
+    """Prefill-sized experts (>= 256 rows each): FC1 on 128-token tiles and
+    FC2 on 256-token tiles with one TMEM accumulator, against the CPU path."""
+    from b200ds.ops import ExpertWeights, QAct, cuda
+    from b200ds.ops.quant import MXFP8Tensor, NVFP4Tensor, dequant_mxfp8
+    import b200ds.ops as ops
+    T, H, I, E, K = 512, 1024, 256, 8, 4            # 256 rows per expert
+    assert cuda.moe_tiles(T * K / E) == (128, 256)
+    torch.manual_seed(7)
+    ids = torch.stack([torch.randperm(E, device=DEV)[:K] for _ in range(T)]).int()
+    wts = torch.rand(T, K, device=DEV)
+    if fp4:
+        ex = ExpertWeights(0, E, _nvfp4_stack(E, 2 * I, H), _nvfp4_stack(E, H, I), I)
+        x = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+        got = cuda.moe_experts_nvfp4(x, wts, ids, ex, torch.float32, n_experts_total=E)
+        cpu = lambda t: NVFP4Tensor(t.data.cpu(), t.sf.cpu(), t.global_scale.cpu(), t.rows)
+        exp = ops.moe_experts(x.float().cpu(), wts.cpu(), ids.cpu(), ExpertWeights(0, E, cpu(ex.w13), cpu(ex.w2), I),
+                              torch.float32)
+        assert rel_err(got.cpu(), exp) < 5e-2, rel_err(got.cpu(), exp)
+        return
+    w13 = [_mx(torch.randn(2 * I, H, device=DEV) * 0.05) for _ in range(E)]
+    w2 = [_mx(torch.randn(H, I, device=DEV) * 0.05) for _ in range(E)]
+    ex = ExpertWeights(0, E, MXFP8Tensor(torch.stack([w.data for w in w13]), torch.stack([w.sf for w in w13])),
+                       MXFP8Tensor(torch.stack([w.data for w in w2]), torch.stack([w.sf for w in w2])), I)
+    a = _mx(torch.randn(T, H, device=DEV))
+    got = cuda.moe_experts(QAct(a.data, a.sf), wts, ids, ex, torch.float32, n_experts_total=E)
+    exc = ExpertWeights(0, E, MXFP8Tensor(ex.w13.data.cpu(), ex.w13.sf.cpu()),
+                        MXFP8Tensor(ex.w2.data.cpu(), ex.w2.sf.cpu()), I)
+    exp = ops.moe_experts(dequant_mxfp8(a.data, a.sf).cpu(), wts.cpu(), ids.cpu(), exc, torch.float32)
+    assert rel_err(got.cpu(), exp) < 3e-2, rel_err(got.cpu(), exp)
