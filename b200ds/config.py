@@ -93,6 +93,15 @@ class ModelConfig:
     engram_clamp: float = 10.0
     # layers whose residual-stream mean is exported (draft-model taps)
     aux_layers: tuple = ()
+    # Compressed sparse attention (V4 family, layers with the indexer): a layer
+    # with ratio r > 1 keeps, per sequence, one compressed latent row per r
+    # consecutive positions - a learned gated mean of their KV rows (weights =
+    # softmax over the block of wgate . x_i + pos_bias[i mod r]) - and compressed
+    # indexer keys made the same way.  A query attends to its sliding window
+    # (the last index_swa positions) plus the compress_topk compressed blocks
+    # before the window that the indexer ranks highest.
+    compress_ratios: tuple = ()      # per layer; 0 or 1 = full resolution
+    compress_topk: int = 512
     # Window-only late layers: layers >= late_layer_start attend to the last
     # late_window positions (up to and including the query) and skip the
     # indexer.  Prefill then needs those layers only on each prompt's tail.
@@ -117,6 +126,13 @@ class ModelConfig:
 
     def is_moe_layer(self, i: int) -> bool:
         return self.n_routed_experts > 0 and i >= self.first_k_dense_replace
+
+    def compress_ratio(self, i: int) -> int:
+        """Compression ratio of layer i (0: full-resolution keys)."""
+        if not self.is_v4 or not self.index_n_heads or self.is_window_layer(i) or i >= len(self.compress_ratios):
+            return 0
+        r = int(self.compress_ratios[i])
+        return r if r > 1 else 0
 
     def is_window_layer(self, i: int) -> bool:
         return self.late_layer_start is not None and self.late_window > 0 and i >= self.late_layer_start

@@ -57,6 +57,9 @@ class V4AttnWeights:
     # indexer's wq_b rows to wq_b)
     ix_k_norm_w: Optional[torch.Tensor] = None
     ix_k_norm_b: Optional[torch.Tensor] = None
+    # compressed sparse attention: the compressor's gate row rides on wqkv_a
+    # (after the indexer rows); per-position-in-block gate bias [ratio]
+    comp_bias: Optional[torch.Tensor] = None
 
 
 @dataclass
@@ -130,21 +133,47 @@ class DeepseekV4Model:
             self.ix_scale = [torch.ones(slots, dtype=torch.float32, device=self.device) for _ in self.layers]
         if c.engram_layers:
             self.tok_cache = torch.full((slots,), -1, dtype=torch.int32, device=self.device)
+        # compressed sparse attention: per compressed layer the gate logit of
+        # every slot, and one compressed latent row / indexer key (+ scale) per
+        # r slots, paged with the same page ids (page_size / r rows a page)
+        self.comp = {}
+        for i in range(len(self.layers)):
+            r = c.compress_ratio(i)
+            if r:
+                if r > 8 or self.page_size % r:
+                    # a block lives in one page; the compressed keys' TMA
+                    # boxes are whole 8-row swizzle atoms
+                    raise ValueError(f"compress ratio {r} must divide the page size and be at most 8")
+                n = slots // r
+                self.comp[i] = dict(
+                    ratio=r,
+                    gate=torch.zeros(slots, dtype=torch.float32, device=self.device),
+                    kv=torch.zeros(n, c.kv_cache_dim, dtype=self.kv_dtype, device=self.device),
+                    ik=torch.zeros(n, c.index_head_dim, dtype=self.kv_dtype, device=self.device),
+                    iks=torch.ones(n, dtype=torch.float32, device=self.device))
 
     def kv_tensors(self) -> List[torch.Tensor]:
-        """Every per-slot cache tensor ([slots, ...], slot = page * page_size +
-        offset): what one KV page holds across the model."""
+        """Every cache tensor indexed by slot (slot = page * page_size +
+        offset) or, for the compressed rows, by page * page_size / r + offset:
+        what one KV page holds across the model."""
         out = list(self.kv_cache)
         out += list(getattr(self, "ix_cache", []) or []) + list(getattr(self, "ix_scale", []) or [])
         if self.tok_cache is not None:
             out.append(self.tok_cache)
+        for cc in getattr(self, "comp", {}).values():
+            out += [cc["gate"], cc["kv"], cc["ik"], cc["iks"]]
         return out
 
     def kv_bytes_per_token(self) -> int:
         c = self.cfg
         es = torch.tensor([], dtype=self.kv_dtype).element_size()
         per = c.kv_cache_dim * es + ((c.index_head_dim * es + 4) if c.index_n_heads else 0)
-        return per * len(self.layers) + (4 if c.engram_layers else 0)
+        total = per * len(self.layers) + (4 if c.engram_layers else 0)
+        for i in range(len(self.layers)):
+            r = c.compress_ratio(i)
+            if r:
+                total += 4 + (c.kv_cache_dim * es + c.index_head_dim * es + 4) // r
+        return total
 
     def vocab_offset(self) -> int:
         rows = getattr(self.lm_head, "rows", None)
@@ -191,7 +220,7 @@ class DeepseekV4Model:
                         self.kv_cache[i], fb.out_slots, self.kv_scale[i], rd)
         qo = aw.wq_b(q_lat, out_dtype=od)
         q = qo[:, : self.heads * L].view(T, self.heads, L)
-        topk = None
+        topk, comp = None, None
         if c.is_window_layer(i):
             # window-only layer: the selection is the last late_window positions
             # (built on the device from the positions, graph-safe)
@@ -203,11 +232,25 @@ class DeepseekV4Model:
             base = ql + L
             ops.index_k_store(qkv[:, base: base + hd], aw.ix_k_norm_w, aw.ix_k_norm_b, 1e-6, self.rope_table,
                               fb.positions, self.ix_cache[i], self.ix_scale[i], fb.out_slots)
-            topk = ops.indexer_topk(qo[:, self.heads * L: self.heads * L + nh * hd], qkv[:, base + hd: base + hd + nh],
-                                    (nh * hd) ** -0.5, self.rope_table, self.ix_cache[i], self.ix_scale[i], fb,
-                                    self.page_size, c.index_topk, c.index_swa)
+            q_ix = qo[:, self.heads * L: self.heads * L + nh * hd]
+            w_ix = qkv[:, base + hd: base + hd + nh]
+            if c.compress_ratio(i):
+                # the gate logits (the row after the indexer's), then the
+                # compressed rows of the blocks this step completes, then the
+                # window + top compressed blocks
+                cc = self.comp[i]
+                ops.compress_store(qkv[:, base + hd + nh], aw.comp_bias, fb, cc["ratio"], self.kv_cache[i],
+                                   self.kv_scale[i], self.ix_cache[i], self.ix_scale[i], cc["gate"], cc["kv"],
+                                   cc["ik"], cc["iks"], self.page_size)
+                topk = ops.indexer_topk_compressed(q_ix, w_ix, (nh * hd) ** -0.5, self.rope_table, cc["ik"],
+                                                   cc["iks"], fb, self.page_size, cc["ratio"], c.compress_topk,
+                                                   c.index_swa)
+                comp = (cc["kv"], cc["ratio"])
+            else:
+                topk = ops.indexer_topk(q_ix, w_ix, (nh * hd) ** -0.5, self.rope_table, self.ix_cache[i],
+                                        self.ix_scale[i], fb, self.page_size, c.index_topk, c.index_swa)
         o = ops.mqa_attention(q, self.kv_cache[i], self.kv_scale[i], fb, c.softmax_scale, self.page_size, aw.sink,
-                              self.rope_table, rd, topk)
+                              self.rope_table, rd, topk, comp=comp)
         z = ops.absorb_o(o.reshape(T, self.groups, -1), aw.wo_a, quantize=aw.wo_b.quantized)
         y = aw.wo_b(z, out_dtype=od)
         return self._reduce(y)
@@ -388,6 +431,8 @@ def build_model_v4(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState, sd: 
             ix = a + "indexer."
             a_rows += [get(ix + "wk.weight"), get(ix + "weights_proj.weight")]
             b_rows += [get(ix + "wq_b.weight")]
+        if cfg.compress_ratio(i):
+            a_rows += [get(a + "compressor.wgate.weight")]
         wo_a = split(get(a + "wo_a.weight").view(G, R, -1), 0, tp, tr).to(dev, wdt).contiguous()
         wo_b = split(get(a + "wo_b.weight"), 1, tp, tr)
         sink = split(get(a + "attn_sink"), 0, tp, tr).to(dev).contiguous() if cfg.attn_sink else None
@@ -398,6 +443,8 @@ def build_model_v4(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState, sd: 
         if cfg.index_n_heads:
             aw.ix_k_norm_w = get(a + "indexer.k_norm.weight").to(dev)
             aw.ix_k_norm_b = get(a + "indexer.k_norm.bias").to(dev)
+        if cfg.compress_ratio(i):
+            aw.comp_bias = get(a + "compressor.pos_bias").float().to(dev).contiguous()
         eng = None
         if i in cfg.engram_layers:
             e = p + "engram."

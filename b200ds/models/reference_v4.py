@@ -90,6 +90,10 @@ def init_weights_v4(cfg: ModelConfig, seed: int = 0, std: float = 0.02) -> Dict[
             sd[ix + "k_norm.weight"] = torch.ones(cfg.index_head_dim)
             sd[ix + "k_norm.bias"] = torch.zeros(cfg.index_head_dim)
             sd[ix + "weights_proj.weight"] = rn(cfg.index_n_heads, h)
+        r = cfg.compress_ratio(i)
+        if r:
+            sd[a + "compressor.wgate.weight"] = rn(1, h)
+            sd[a + "compressor.pos_bias"] = rn(r, s=0.5)
         m = p + "mlp."
         if cfg.is_moe_layer(i):
             sd[m + "gate.weight"] = rn(cfg.n_routed_experts, h)
@@ -152,6 +156,7 @@ class ReferenceV4Model:
         c = self.cfg
         self.cache = [torch.zeros(batch, self.max_len, c.kv_lora_rank) for _ in range(c.num_hidden_layers)]
         self.ik = [torch.zeros(batch, self.max_len, c.index_head_dim) for _ in range(c.num_hidden_layers)]
+        self.gate = [torch.zeros(batch, self.max_len) for _ in range(c.num_hidden_layers)]
         self.tokens = torch.full((batch, self.max_len), -1, dtype=torch.int64)
 
     # -- mHC ------------------------------------------------------------------
@@ -179,6 +184,9 @@ class ReferenceV4Model:
         end = start + S
         self.cache[i][:, start:end] = kv
         keys = self.cache[i][:, :end]                                          # [B, end, L]
+        if c.compress_ratio(i):
+            o = self._compressed_attn(i, x, qr, q, keys, pos, start, S)
+            return self._attn_out(i, o, pos)
         s = torch.einsum("bshd,bld->bhsl", q, keys) * c.softmax_scale
         causal = torch.arange(end).view(1, end) <= (start + torch.arange(S)).view(S, 1)
         mask = causal.view(1, 1, S, end)
@@ -194,12 +202,77 @@ class ReferenceV4Model:
         else:
             p = s.softmax(-1)
         o = torch.einsum("bhsl,bld->bshd", p, keys)                          # [B, S, H, L]
+        return self._attn_out(i, o, pos)
+
+    def _attn_out(self, i: int, o: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        """Inverse RoPE of the output tails, grouped wo_a, wo_b."""
+        c, w = self.cfg, self.w
+        a = f"model.layers.{i}.self_attn."
+        B, S, H, L = o.shape
+        rd = c.qk_rope_head_dim
         o = ref.inv_rope_tail(o.reshape(B * S, H, L), pos.repeat(B), self.rope, rd).view(B, S, H, L)
         G, R = c.o_groups, c.o_lora_rank
         og = o.reshape(B, S, G, (H // G) * L)
         wa = w[a + "wo_a.weight"].view(G, R, (H // G) * L)
         z = torch.einsum("bsgk,grk->bsgr", og, wa).reshape(B, S, G * R)
         return z @ w[a + "wo_b.weight"].T
+
+    def _compressed_attn(self, i, x, qr, q, keys, pos, start, S):
+        """Compressed sparse attention of layer i (ratio r): every query
+        attends to its window (the last index_swa positions) plus the
+        compress_topk compressed blocks before the window with the highest
+        indexer scores; a block's row is the gated mean of its r KV rows
+        (softmax over the block of wgate . x + pos_bias), its indexer key
+        the same mean of the r indexer keys.  Returns o [B, S, H, L]."""
+        import torch.nn.functional as F
+        from .rope import apply_rope_ref
+        c, w = self.cfg, self.w
+        a = f"model.layers.{i}.self_attn."
+        B, end = keys.shape[0], start + S
+        r, swa = c.compress_ratio(i), c.index_swa
+        H, L = c.num_attention_heads, c.kv_lora_rank
+        nh, hd, rd = c.index_n_heads, c.index_head_dim, c.qk_rope_head_dim
+        # gates, indexer queries / keys / head weights
+        self.gate[i][:, start:end] = (x @ w[a + "compressor.wgate.weight"].T)[..., 0]
+        ix = a + "indexer."
+        qi = (qr @ w[ix + "wq_b.weight"].T).view(B, S, nh, hd)
+        qi = torch.cat([apply_rope_ref(qi[..., :rd], pos.expand(B, S), self.rope), qi[..., rd:]], -1)
+        k = F.layer_norm(x @ w[ix + "wk.weight"].T, (hd,), w[ix + "k_norm.weight"], w[ix + "k_norm.bias"], 1e-6)
+        k = torch.cat([apply_rope_ref(k[..., :rd], pos.expand(B, S), self.rope), k[..., rd:]], -1)
+        self.ik[i][:, start:end] = k
+        hw = (x @ w[ix + "weights_proj.weight"].T) * (nh ** -0.5) * (hd ** -0.5)
+        # compressed rows of the complete blocks
+        nb = end // r
+        g = self.gate[i][:, :nb * r].view(B, nb, r) + w[a + "compressor.pos_bias"].view(1, 1, r)
+        wt = torch.softmax(g, -1).unsqueeze(-1)
+        ckv = (wt * keys[:, :nb * r].view(B, nb, r, L)).sum(2)                        # [B, nb, L]
+        cik = (wt * self.ik[i][:, :nb * r].view(B, nb, r, hd)).sum(2)                # [B, nb, hd]
+        qpos = (start + torch.arange(S)).view(S, 1)
+        # window mask over full-resolution keys
+        j = torch.arange(end).view(1, end)
+        win = (j <= qpos) & (j > qpos - swa)                                           # [S, end]
+        # candidate blocks (entirely before the window) and their top-k
+        jb = torch.arange(nb).view(1, nb)
+        cand = jb < (qpos + 1 - swa) // r                                              # [S, nb]
+        sc = (torch.einsum("bshd,bjd->bshj", qi, cik).relu() * hw.unsqueeze(-1)).sum(2)  # [B, S, nb]
+        sc = sc.masked_fill(~cand.unsqueeze(0), float("-inf"))
+        sel = torch.zeros(B, S, nb, dtype=torch.bool)
+        if nb:
+            kk = min(c.compress_topk, nb)
+            idx = sc.topk(kk, dim=-1).indices
+            sel = sel.scatter_(2, idx, True) & cand.unsqueeze(0)
+        s_w = torch.einsum("bshd,bld->bhsl", q, keys) * c.softmax_scale
+        s_w = s_w.masked_fill(~win.view(1, 1, S, end), float("-inf"))
+        s_c = torch.einsum("bshd,bjd->bhsj", q, ckv) * c.softmax_scale
+        s_c = s_c.masked_fill(~sel.unsqueeze(1), float("-inf"))
+        s_all = torch.cat([s_w, s_c], -1)
+        if c.attn_sink:
+            sink = w[a + "attn_sink"].view(1, H, 1, 1).expand(B, H, S, 1)
+            p = torch.cat([s_all, sink], -1).softmax(-1)[..., :-1]
+        else:
+            p = s_all.softmax(-1)
+        return (torch.einsum("bhsl,bld->bshd", p[..., :end], keys)
+                + torch.einsum("bhsj,bjd->bshd", p[..., end:], ckv))
 
     def _indexer_select(self, i, x, qr, pos, start, S):
         """Lightning indexer (as the V3.2 oracle) plus the sliding window:

@@ -570,18 +570,50 @@ def kv_store_v4(kv: torch.Tensor, w: torch.Tensor, eps: float, table: torch.Tens
 
 
 def mqa_attention(q: torch.Tensor, cache: torch.Tensor, kv_scale: float, fb, softmax_scale: float, page_size: int,
-                  sink: Optional[torch.Tensor], table: torch.Tensor, rd: int, topk=None) -> torch.Tensor:
+                  sink: Optional[torch.Tensor], table: torch.Tensor, rd: int, topk=None, comp=None) -> torch.Tensor:
     """MQA over the paged latent rows (K = V = row[:L]) with RoPE on the
     query tails, per-head sinks, and the output tails rotated back to
-    position 0.  q [T, H, L] -> o [T, H, L]."""
+    position 0.  q [T, H, L] -> o [T, H, L].  comp = (compressed rows,
+    ratio): selection entries >= ref.COMP_FLAG name compressed blocks."""
     if _use_native(q):
-        return _native().mqa_attention(q, cache, kv_scale, fb, softmax_scale, page_size, sink, table, rd, topk)
+        return _native().mqa_attention(q, cache, kv_scale, fb, softmax_scale, page_size, sink, table, rd, topk,
+                                       comp=comp)
     T, H, L = q.shape
     qf = q.float()
     qf = torch.cat([qf[..., :L - rd], ref.rope(qf[..., L - rd:], fb.positions, table)], -1)
     o = ref.mqa_sink_attention(qf, cache, kv_scale, fb.block_table, fb.q_seq, fb.positions, softmax_scale, page_size,
-                               sink, L, topk)
+                               sink, L, topk, comp=comp)
     return ref.inv_rope_tail(o, fb.positions, table, rd)
+
+
+def compress_store(g: torch.Tensor, bias: torch.Tensor, fb, r: int, kv_cache: torch.Tensor, kv_scale: float,
+                   ix_cache: torch.Tensor, ix_scale: torch.Tensor, gate: torch.Tensor, ckv: torch.Tensor,
+                   cik: torch.Tensor, cis: torch.Tensor, page_size: int) -> None:
+    """Compressed attention: store this step's gate logits g [T] and write
+    the compressed latent rows / indexer keys of the blocks the step
+    completes (ref.compress_store)."""
+    if _use_native(kv_cache):
+        return _native().compress_store(g, bias, fb, r, kv_cache, kv_scale, ix_cache, ix_scale, gate, ckv, cik, cis,
+                                        page_size)
+    ref.compress_store(to_float(g), bias, fb.positions, fb.out_slots, fb.q_seq, fb.block_table, r, kv_cache,
+                       kv_scale, ix_cache, ix_scale, gate, ckv, cik, cis, page_size)
+
+
+def indexer_topk_compressed(q_raw, w_raw, w_factor: float, table, cik, cis, fb, page_size: int, r: int, topk: int,
+                            swa: int):
+    """Selection of a compressed-attention layer [T, swa + topk]: the window
+    positions, then the indexer's top compressed blocks before the window
+    (entries COMP_FLAG + block)."""
+    if _use_native(q_raw):
+        return _native().indexer_topk_compressed(q_raw, w_raw, w_factor, table, cik, cis, fb, page_size, r, topk,
+                                                 swa)
+    T, nh = w_raw.shape
+    rd = table.shape[-1]
+    q = to_float(q_raw).reshape(T, nh, -1)
+    q = torch.cat([ref_rope(q[..., :rd], fb.positions, table), q[..., rd:]], -1)
+    w = to_float(w_raw) * w_factor
+    return ref.indexer_select_compressed(q, w, cik, cis, fb.block_table, fb.q_seq, fb.positions, page_size, r,
+                                         topk, swa)
 
 
 def e5_prune(w: torch.Tensor, ids: torch.Tensor, cfg, n_experts: int):

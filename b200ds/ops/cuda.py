@@ -284,7 +284,7 @@ def mla_attention(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size, to
     return _mla_core(q8, qs, cache, kv_scale, fb, softmax_scale, page_size, topk)
 
 
-def _mla_core(q8, qs, cache, kv_scale, fb, softmax_scale, page_size, topk, lse_out=None):
+def _mla_core(q8, qs, cache, kv_scale, fb, softmax_scale, page_size, topk, lse_out=None, comp=None):
     T, H, _ = q8.shape
     L = 512
     dev = q8.device
@@ -298,6 +298,13 @@ def _mla_core(q8, qs, cache, kv_scale, fb, softmax_scale, page_size, topk, lse_o
     if nsplit > 1:
         po = torch.empty(nsplit, T, H, L, dtype=torch.float32, device=dev)
         pl = torch.empty(nsplit, T, H, dtype=torch.float32, device=dev)
+    if comp is not None:
+        # compressed blocks (entries >= COMP_FLAG) are gathered from the
+        # compressed rows; the selection keeps them in aligned groups of four
+        _C.mla_tc(q8, qs, cache.view(torch.uint8), kv_scale, fb.block_table, fb.q_seq, fb.positions, page_size,
+                  softmax_scale, nsplit, out, po, pl, topk, mla_hb(H), lse_out=lse_out,
+                  cache2=comp[0].view(torch.uint8), ratio2=int(comp[1]))
+        return out
     _C.mla_tc(q8, qs, cache.view(torch.uint8), kv_scale, fb.block_table, fb.q_seq, fb.positions, page_size,
               softmax_scale, nsplit, out, po, pl, topk, mla_hb(H), lse_out=lse_out)
     return out
@@ -665,6 +672,50 @@ def indexer_topk(q_raw, w_raw, w_factor, table, k_cache, k_scale, fb, page_size,
     return out
 
 
+def indexer_topk_compressed(q_raw, w_raw, w_factor, table, cik, cis, fb, page_size, r, topk, swa):
+    """Selection of a compressed-attention layer [T, swa + topk]: the window
+    (built on the device from the positions), then the indexer's top blocks
+    among those ending before the window: tcgen05 scores over the compressed
+    keys (paged page_size / r rows a page, key j of sequence b at
+    table[b, j*r // page] * (page / r) + j mod (page / r)) and the radix
+    top-k, tagged COMP_FLAG + block."""
+    from .ref import COMP_FLAG
+    T, nh = w_raw.shape
+    dev = q_raw.device
+    if swa % 4 or topk % 4:
+        raise ValueError("compressed attention needs window and top-k sizes that are multiples of 4")
+    cpg = page_size // r
+    cap = int(fb.block_table.shape[1]) * cpg
+    pos = fb.positions
+    out = torch.empty(T, swa + topk, dtype=torch.int32, device=dev)
+    win = pos.view(-1, 1) - (swa - 1) + torch.arange(swa, dtype=torch.int32, device=dev)
+    out[:, :swa] = torch.where(win >= 0, win, torch.full_like(win, -1))
+    # last whole block before the window (-1: none yet)
+    cpos = (torch.div(pos + 1 - swa, r, rounding_mode="floor") - 1).clamp(min=-1).to(torch.int32)
+    ck = cik.view(torch.uint8)
+    step = max(1, min(T, _IX_SCORE_BYTES // (cap * 4)))
+    max_len = max(1, (int(fb.max_seq_len) if fb.max_seq_len else cap * r) // r)
+    sel = torch.empty(T, topk, dtype=torch.int32, device=dev)
+    for t0 in range(0, T, step):
+        t1 = min(T, t0 + step)
+        n = t1 - t0
+        q8 = torch.empty(n * nh, 128, dtype=torch.uint8, device=dev)
+        wq = torch.empty(n, nh, dtype=torch.float32, device=dev)
+        _C.ix_q_quant(q_raw[t0:t1], w_raw[t0:t1], nh, w_factor, pos[t0:t1], table, q8, wq)
+        scores = torch.empty(n, cap, dtype=torch.float32, device=dev)
+        _C.ix_score(q8, wq, ck, cis, fb.block_table, fb.q_seq[t0:t1], cpos[t0:t1], cpg, ix_splits(n, max_len),
+                    scores)
+        _C.topk_select(scores, cpos[t0:t1], sel[t0:t1])
+    out[:, swa:] = torch.where(sel >= 0, sel + COMP_FLAG, torch.full_like(sel, -1))
+    return out
+
+
+def compress_store(g, bias, fb, r, kv_cache, kv_scale, ix_cache, ix_scale, gate, ckv, cik, cis, page_size):
+    _C.compress_store(g, bias, fb.positions, fb.out_slots, fb.q_seq, fb.block_table, page_size, r,
+                      kv_cache.view(torch.uint8), kv_scale, ix_cache.view(torch.uint8), ix_scale, gate,
+                      ckv.view(torch.uint8), cik.view(torch.uint8), cis)
+
+
 SAMPLE_CANDIDATES = 64
 
 
@@ -792,7 +843,7 @@ def kv_store_v4(kv, w, eps, table, pos, cache, slots, kv_scale, rd):
     _C.kv_store_v4(kv, w, eps, pos, table, cache.view(torch.uint8), slots, kv_scale, rd)
 
 
-def mqa_attention(q, cache, kv_scale, fb, softmax_scale, page_size, sink, table, rd, topk=None):
+def mqa_attention(q, cache, kv_scale, fb, softmax_scale, page_size, sink, table, rd, topk=None, comp=None):
     """Heads per rank below a multiple of 16 (e.g. 64 heads over 8 ranks) are
     padded with zero queries up to the latent-attention kernel's head block;
     the padded heads' outputs are dropped."""
@@ -804,7 +855,7 @@ def mqa_attention(q, cache, kv_scale, fb, softmax_scale, page_size, sink, table,
     qb = q if q.dtype == torch.bfloat16 else q.to(torch.bfloat16)
     _C.mqa_q_prep(qb, fb.positions, table, rd, q8, qs)
     lse = torch.empty(T, Hp, dtype=torch.float32, device=dev) if sink is not None else None
-    out = _mla_core(q8, qs, cache, kv_scale, fb, softmax_scale, page_size, topk, lse_out=lse)
+    out = _mla_core(q8, qs, cache, kv_scale, fb, softmax_scale, page_size, topk, lse_out=lse, comp=comp)
     if Hp != H and sink is not None:
         sink = torch.cat([sink.float(), sink.new_zeros(Hp - H)])
     _C.attn_fixup(out, lse, sink, rd, fb.positions, table)

@@ -295,24 +295,47 @@ def e5_prune(ids: torch.Tensor, w: torch.Tensor, budget: float, max_count: int):
     return w, ids
 
 
+# A selection entry with this bit set names compressed block j = entry - COMP_FLAG
+# of a compressed-attention layer (its row in the compressed cache), not a
+# full-resolution position.
+COMP_FLAG = 1 << 30
+
+
+def comp_rows(block_table: torch.Tensor, b: int, j: torch.Tensor, r: int, page_size: int) -> torch.Tensor:
+    """Rows of compressed blocks j of sequence b: block j covers positions
+    j*r .. j*r + r - 1 (one page), stored at page * (page_size / r) +
+    (j*r mod page_size) / r of the compressed tensors."""
+    p0 = j.long() * r
+    return block_table[b, (p0 // page_size).long()].long() * (page_size // r) + (p0 % page_size) // r
+
+
 def mqa_sink_attention(q: torch.Tensor, kv_cache: torch.Tensor, kv_scale: float, block_table: torch.Tensor,
                        q_seq: torch.Tensor, q_pos: torch.Tensor, softmax_scale: float, page_size: int,
                        sink: Optional[torch.Tensor], L: int,
-                       topk_idx: Optional[torch.Tensor] = None) -> torch.Tensor:
+                       topk_idx: Optional[torch.Tensor] = None, comp=None) -> torch.Tensor:
     """MQA over the paged latent rows: K = V = cache[:, :L]; q [T, H, L];
-    sink [H] (natural-log logits joining each head's softmax denominator)."""
+    sink [H] (natural-log logits joining each head's softmax denominator).
+    comp = (compressed rows, ratio): selection entries >= COMP_FLAG name
+    compressed blocks (compressed attention)."""
     T, H, _ = q.shape
     out = torch.zeros(T, H, L, dtype=torch.float32, device=q.device)
     kvf = kv_cache.float() * kv_scale
+    ckf = comp[0].float() * kv_scale if comp is not None else None
     for t in range(T):
         b = int(q_seq[t])
         n = int(q_pos[t]) + 1
         pos = torch.arange(n, device=q.device)
+        kc = None
         if topk_idx is not None:
-            sel = topk_idx[t]
+            sel = topk_idx[t].long()
+            if comp is not None:
+                cj = sel[sel >= COMP_FLAG] - COMP_FLAG
+                kc = ckf[comp_rows(block_table, b, cj, comp[1], page_size)][:, :L]
             pos = sel[(sel >= 0) & (sel < n)].long()
         pages = block_table[b, (pos // page_size).long()].long()
         k = kvf[pages * page_size + pos % page_size][:, :L]
+        if kc is not None:
+            k = torch.cat([k, kc], 0)
         s = (q[t].float() @ k.T) * softmax_scale                       # [H, n]
         if sink is not None:
             s = torch.cat([s, sink.float().unsqueeze(-1)], -1)
@@ -403,3 +426,63 @@ def inv_rope_tail(o: torch.Tensor, pos: torch.Tensor, table: torch.Tensor, rd: i
     neg = torch.cat([cs[:, : rd // 2], -cs[:, rd // 2:]], -1)
     tail = rope(o[..., -rd:], torch.arange(o.shape[0]), neg)
     return torch.cat([o[..., :-rd].float(), tail], -1)
+
+
+def compress_store(g: torch.Tensor, bias: torch.Tensor, positions: torch.Tensor, out_slots: torch.Tensor,
+                   q_seq: torch.Tensor, block_table: torch.Tensor, r: int, kv_cache: torch.Tensor, kv_scale: float,
+                   ix_cache: torch.Tensor, ix_scale: torch.Tensor, gate: torch.Tensor, ckv: torch.Tensor,
+                   cik: torch.Tensor, cis: torch.Tensor, page_size: int) -> None:
+    """Compressor: store each row's gate logit g[t] at its slot; for every row
+    that completes a block (position p with (p + 1) % r == 0), write block
+    j = p // r's compressed latent row (softmax over the block of gate +
+    bias[i mod r] weighting its r cached rows; same scale as the cache) and
+    compressed indexer key (own per-row scale amax / 448 for e4m3)."""
+    gate[out_slots.long()] = g.float()
+    fp8 = kv_cache.dtype == torch.float8_e4m3fn
+    for t in range(positions.shape[0]):
+        p = int(positions[t])
+        if (p + 1) % r:
+            continue
+        b = int(q_seq[t])
+        pos = torch.arange(p + 1 - r, p + 1, device=positions.device)
+        slots = block_table[b, (pos // page_size).long()].long() * page_size + pos % page_size
+        w = torch.softmax(gate[slots].float() + bias.float(), 0).unsqueeze(-1)
+        kv = (w * (kv_cache[slots].float() * kv_scale)).sum(0)
+        ik = (w * (ix_cache[slots].float() * ix_scale[slots].float().unsqueeze(-1))).sum(0)
+        row = int(comp_rows(block_table, b, torch.tensor([p // r], device=positions.device), r, page_size)[0])
+        ckv[row] = (kv / kv_scale).to(ckv.dtype)
+        if fp8:
+            s = ik.abs().amax().clamp(min=1e-12) / 448.0
+            cik[row] = (ik / s).to(cik.dtype)
+            cis[row] = s
+        else:
+            cik[row] = ik.to(cik.dtype)
+            cis[row] = 1.0
+
+
+def indexer_select_compressed(q: torch.Tensor, w: torch.Tensor, cik: torch.Tensor, cis: torch.Tensor,
+                              block_table: torch.Tensor, q_seq: torch.Tensor, q_pos: torch.Tensor, page_size: int,
+                              r: int, topk: int, swa: int) -> torch.Tensor:
+    """Selection of a compressed-attention layer: per query at position p,
+    its window positions p - swa + 1 .. p (-1 before position 0) followed by
+    the top-`topk` compressed blocks j < (p + 1 - swa) // r by indexer score
+    sum_h w[t,h] relu(q[t,h] . key_j) (entries COMP_FLAG + j, -1 padded).
+    Returns int32 [T, swa + topk]."""
+    T = q.shape[0]
+    out = torch.full((T, swa + topk), -1, dtype=torch.int32, device=q.device)
+    for t in range(T):
+        b = int(q_seq[t])
+        p = int(q_pos[t])
+        win = torch.arange(p - swa + 1, p + 1, device=q.device)
+        out[t, :swa] = torch.where(win >= 0, win, torch.full_like(win, -1)).to(torch.int32)
+        nc = max(0, (p + 1 - swa) // r)
+        if nc == 0:
+            continue
+        j = torch.arange(nc, device=q.device)
+        rows = comp_rows(block_table, b, j, r, page_size)
+        k = cik[rows].float() * cis[rows].float().unsqueeze(-1)
+        sc = ((q[t].float() @ k.T).relu() * w[t].float().unsqueeze(-1)).sum(0)
+        kk = min(topk, nc)
+        idx = sc.topk(kk).indices.sort().values
+        out[t, swa: swa + kk] = (idx + COMP_FLAG).to(torch.int32)
+    return out

@@ -360,9 +360,7 @@ def main():
                        "context_points": per_point,
                        "parallelism": (f"dp{world}-attn+ep{world}-moe" if args.dp else f"tp{world}-attn+ep{world}-moe"),
                        "expert_format": cfg.expert_format, "weight_sets": getattr(model, "weight_sets", None),
-                       "weight_format": "e4m3 weights with one UE8M0 scale per 32 K elements (MXFP8; the "
-                                        "checkpoint's 128x128 fp32 block scales are converted at load) and "
-                                        "activations quantized the same way per 32 (the config's 1x128)",
+                       "weight_format": weight_format(cfg, args.impl),
                        "switches": __import__("b200ds.utils.levers", fromlist=["switches"]).switches(),
                        "selfcheck": eng.selfcheck,
                        "l2": "no flush: per-step weights+KV >> 126 MB L2", "init_s": round(t_init, 1)},
@@ -390,6 +388,19 @@ def main():
         except Exception as e:
             log(f"process-group teardown: {e}")
         wd.cancel()
+
+
+def weight_format(cfg, impl: str) -> str:
+    """The weight / activation formats the timed step streams."""
+    dense = ("dense and attention weights e4m3 with one UE8M0 scale per 32 K elements (MXFP8; a checkpoint's "
+             "128x128 fp32 block scales are converted at load), activations quantized the same way per 32")
+    if impl == "baseline":
+        return ("routed experts: the same e4m3 bytes with 128x128 fp32 block scales, activations with 1x128 scales "
+                "(FlashInfer trtllm-gen DeepSeek FP8); " + dense)
+    if cfg.expert_format == "nvfp4":
+        return ("routed experts NVFP4 (e2m1 + e4m3 per 16 + fp32 global scale per expert; activations per token); "
+                + dense)
+    return "routed experts and " + dense
 
 
 def context_points(input_len: int, output_len: int, steps: int, warmup: int):

@@ -29,7 +29,14 @@ struct MlaTcArgs {
   int topk_n = 0;
   int hb = 0;                 // heads per CTA (16 / 32 / 64); 0 = largest that divides H
   float* lse_out = nullptr;   // [T, H] log-sum-exp (log2 of the sum of 2^(scaled score)), optional
+  // compressed sparse attention: top-k entries >= kMlaCompFlag name compressed
+  // block j = entry - kMlaCompFlag, whose row (same e4m3 layout and scale) is
+  // page * (64 / ratio) + (j * ratio mod 64) / ratio of cache2
+  const uint8_t* cache2 = nullptr;
+  int64_t cache2_rows = 0;
+  int ratio2 = 0;
 };
+constexpr int kMlaCompFlag = 1 << 30;
 // Lightning indexer (sparse MLA): key store, query quantisation, tcgen05
 // scores and the top-k radix select.
 int b200_ix_k_store(const void* k, int f32, int64_t ld, int T, const float* ln_w, const float* ln_b, float eps,

@@ -59,7 +59,7 @@ void mla_tc(const at::Tensor& q8, const at::Tensor& qs, const at::Tensor& cache,
             const at::Tensor& block_table, const at::Tensor& q_seq, const at::Tensor& q_pos, int64_t page_size,
             double sm_scale, int64_t nsplit, at::Tensor out, c10::optional<at::Tensor> part_o,
             c10::optional<at::Tensor> part_lse, c10::optional<at::Tensor> topk, int64_t hb,
-            c10::optional<at::Tensor> lse_out) {
+            c10::optional<at::Tensor> lse_out, c10::optional<at::Tensor> cache2, int64_t ratio2) {
   TORCH_CHECK(q8.is_cuda() && q8.dim() == 3 && q8.size(2) == 576 && q8.is_contiguous(), "q8 e4m3 [T,H,576]");
   TORCH_CHECK(cache.dim() == 2 && cache.size(1) == 576 && cache.is_contiguous(), "cache [slots, 576]");
   TORCH_CHECK(block_table.scalar_type() == at::kInt && q_seq.scalar_type() == at::kInt && q_pos.scalar_type() == at::kInt,
@@ -86,6 +86,13 @@ void mla_tc(const at::Tensor& q8, const at::Tensor& qs, const at::Tensor& cache,
   a.sm_scale = sm_scale;
   a.kv_scale = kv_scale;
   a.out = out.data_ptr();
+  if (cache2.has_value() && cache2->defined()) {
+    TORCH_CHECK(cache2->dim() == 2 && cache2->size(1) == 576 && cache2->is_contiguous() && ratio2 >= 2 &&
+                    64 % ratio2 == 0, "cache2 [rows, 576] with ratio2 in 2..64 dividing 64");
+    a.cache2 = reinterpret_cast<const uint8_t*>(cache2->data_ptr());
+    a.cache2_rows = cache2->size(0);
+    a.ratio2 = int(ratio2);
+  }
   if (nsplit > 1) {
     TORCH_CHECK(part_o.has_value() && part_lse.has_value(), "split partial buffers");
     a.part_o = reinterpret_cast<float*>(part_o->data_ptr());
@@ -165,7 +172,7 @@ void register_attn(pybind11::module& m) {
         pybind11::arg("block_table"), pybind11::arg("q_seq"), pybind11::arg("q_pos"), pybind11::arg("page_size"),
         pybind11::arg("sm_scale"), pybind11::arg("nsplit"), pybind11::arg("out"), pybind11::arg("part_o"),
         pybind11::arg("part_lse"), pybind11::arg("topk") = pybind11::none(), pybind11::arg("hb") = 0,
-        pybind11::arg("lse_out") = pybind11::none());
+        pybind11::arg("lse_out") = pybind11::none(), pybind11::arg("cache2") = pybind11::none(), pybind11::arg("ratio2") = 0);
   m.def("ix_k_store", &ix_k_store);
   m.def("ix_q_quant", &ix_q_quant);
   m.def("ix_score", &ix_score);

@@ -33,7 +33,7 @@ namespace b200 {
 namespace ix {
 
 constexpr int kD = 128;          // indexer head dim (bytes per e4m3 key)
-constexpr int kPage = 64;        // tokens per cache page
+// cache pages hold 64 token rows (compressed key caches 64 / r rows, same page ids)
 constexpr int kTile = 128;       // keys per MMA tile
 constexpr int kThreads = 192;
 constexpr int kStages = 4;
@@ -141,6 +141,7 @@ struct ScoreParams {
   int bt_stride;
   const int* q_seq;
   const int* q_pos;
+  int page;                 // key rows per cache page (64; 64 / r for compressed keys)
   int nsplit;
   float* scores;            // [T, ld]
   int64_t ld;
@@ -206,10 +207,10 @@ ix_score_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         if (i >= kStages && !mbar_wait(&k_empty[s], ((i / kStages) - 1) & 1, p.err)) break;
         mbar_arrive_expect_tx(&k_full[s], S::kK);
         const int tok0 = k_lo + i * kTile;
-        for (int pg = 0; pg < 2; ++pg) {
-          const int tk = tok0 + pg * kPage;
-          const int page = tk < n ? p.block_table[(int64_t)b * p.bt_stride + tk / kPage] : 0;
-          tma_load_2d(sK + s * S::kK + pg * kPage * kD, &tm_k, &k_full[s], 0, page * kPage);
+        for (int pg = 0; pg < kTile / p.page; ++pg) {
+          const int tk = tok0 + pg * p.page;
+          const int page = tk < n ? p.block_table[(int64_t)b * p.bt_stride + tk / p.page] : 0;
+          tma_load_2d(sK + s * S::kK + pg * p.page * kD, &tm_k, &k_full[s], 0, page * p.page);
         }
       }
     }
@@ -254,7 +255,7 @@ ix_score_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       if (lane == 0) mbar_arrive(&acc_empty[a]);
       const int key = k_lo + i * kTile + row;
       if (key < k_hi) {
-        const int64_t slot = (int64_t)p.block_table[(int64_t)b * p.bt_stride + key / kPage] * kPage + key % kPage;
+        const int64_t slot = (int64_t)p.block_table[(int64_t)b * p.bt_stride + key / p.page] * p.page + key % p.page;
         p.scores[(int64_t)t * p.ld + key] = acc * p.k_scale[slot];
       }
     }
@@ -341,12 +342,16 @@ int b200_ix_score(const uint8_t* q8, const float* wq, int T, int NH, const uint8
                   int page_size, int nsplit, float* scores, int64_t ld, uint32_t* err, cudaStream_t st) {
   using namespace b200::ix;
   if (T <= 0) return 0;
-  if (page_size != kPage || NH != 64 || nsplit < 1) return -1;
+  // page_size: key rows per page (64; 32 / 16 / 8 for keys compressed 2x /
+  // 4x / 8x, paged with the same page ids); a 128-key tile loads 128 /
+  // page_size boxes, each a whole number of 1 KB swizzle atoms
+  if (page_size < 8 || 64 % page_size || NH != 64 || nsplit < 1) return -1;
   using S = ScoreSmem<64>;
   CUtensorMap mq, mk;
   if (map_rows128(&mq, q8, (int64_t)T * NH, NH)) return -2;
-  if (map_rows128(&mk, k_cache, cache_rows, kPage)) return -3;
+  if (map_rows128(&mk, k_cache, cache_rows, page_size)) return -3;
   ScoreParams p{};
+  p.page = page_size;
   p.wq = wq;
   p.k_scale = k_scale;
   p.block_table = block_table;

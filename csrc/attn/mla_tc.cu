@@ -102,6 +102,7 @@ struct Params {
   const uint8_t* cache;      // e4m3 [rows, 576] (sparse gathers)
   const int* topk;           // [T, topk_n] cache positions, -1 = none (sparse)
   int topk_n;
+  int ratio2;                // compressed rows (entries >= kMlaCompFlag) in the second cache, 0 = none
 };
 
 __device__ __forceinline__ void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
@@ -136,6 +137,7 @@ template <int HB, bool SPARSE>
 __global__ void __launch_bounds__(kThreads, 1)
 mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constant__ CUtensorMap tm_q_rope,
               const __grid_constant__ CUtensorMap tm_kv_lat, const __grid_constant__ CUtensorMap tm_kv_rope,
+              const __grid_constant__ CUtensorMap tm_c_lat, const __grid_constant__ CUtensorMap tm_c_rope,
               Params p) {
   using S = Smem<HB>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -222,39 +224,74 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
         const int tok0 = k_lo + i * kTile;
         if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], S::kKVStage);
         __syncwarp();
-        int rows[4];
+        int ent[4], rows[4];
+        bool comp = false;
 #pragma unroll
         for (int m = 0; m < 4; ++m) {
           const int j = tok0 + 4 * lane + m;                 // list entry of tile row 4 lane + m
-          const int pos = j < k_hi ? __ldcg(list + j) : -1;
-          rows[m] = (pos >= 0 && pos < n)
-                        ? __ldcg(p.block_table + (int64_t)b * p.bt_stride + pos / kPage) * kPage + pos % kPage
-                        : int(row0);
+          ent[m] = j < k_hi ? __ldcg(list + j) : -1;
+          comp |= (p.ratio2 > 0 && ent[m] >= kMlaCompFlag);
         }
+        // a group of four entries reads one cache: compressed blocks (entries
+        // >= kMlaCompFlag; the selection keeps them in groups of four after
+        // the window) or full-resolution positions; a group's empty entries
+        // read that cache's first row and are masked by the softmax
+        const int cpage = comp ? kPage / p.ratio2 : kPage;
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          if (comp) {
+            const int jb = ent[m] >= kMlaCompFlag ? ent[m] - kMlaCompFlag : 0;
+            const int q0 = jb * p.ratio2;
+            rows[m] = __ldcg(p.block_table + (int64_t)b * p.bt_stride + q0 / kPage) * cpage + (q0 % kPage) / p.ratio2;
+          } else {
+            rows[m] = (ent[m] >= 0 && ent[m] < n)
+                          ? __ldcg(p.block_table + (int64_t)b * p.bt_stride + ent[m] / kPage) * kPage + ent[m] % kPage
+                          : int(row0);
+          }
+        }
+        const CUtensorMap* ml = comp ? &tm_c_lat : &tm_kv_lat;
+        const CUtensorMap* mr = comp ? &tm_c_rope : &tm_kv_rope;
 #pragma unroll
         for (int c = 0; c < 4; ++c)                          // latent: 4 boxes of 128 B
-          tma_gather4(dst + c * kTile * 128 + 4 * lane * 128, &tm_kv_lat, &kv_full[s], c * 128, rows);
-        tma_gather4(dst + S::kKVLat + 4 * lane * 64, &tm_kv_rope, &kv_full[s], kL, rows);
+          tma_gather4(dst + c * kTile * 128 + 4 * lane * 128, ml, &kv_full[s], c * 128, rows);
+        tma_gather4(dst + S::kKVLat + 4 * lane * 64, mr, &kv_full[s], kL, rows);
       }
-    } else if (!SPARSE && lane == 0 && nt > 0) {
-      const int qrow = t * p.H + h0;
-      mbar_arrive_expect_tx(q_full, S::kQLat + S::kQRope);
-      for (int c = 0; c < 4; ++c) tma_load_2d(sQ + c * HB * 128, &tm_q_lat, q_full, c * 128, qrow);
-      tma_load_2d(sQ + S::kQLat, &tm_q_rope, q_full, kL, qrow);
+    } else if (!SPARSE && nt > 0) {
+      // The warp reads the split's page ids 32 at a time (lane l holds the
+      // page of logical page lp0 + 32 w + l) ahead of the tiles that use
+      // them, so no block-table load sits between a stage's release and its
+      // next TMA issue; lane 0 issues the loads.
+      if (lane == 0) {
+        const int qrow = t * p.H + h0;
+        mbar_arrive_expect_tx(q_full, S::kQLat + S::kQRope);
+        for (int c = 0; c < 4; ++c) tma_load_2d(sQ + c * HB * 128, &tm_q_lat, q_full, c * 128, qrow);
+        tma_load_2d(sQ + S::kQLat, &tm_q_rope, q_full, kL, qrow);
+      }
+      const int* btr = p.block_table + (int64_t)b * p.bt_stride;
+      const int lp0 = k_lo / kPage;                  // k_lo is a multiple of the 128-token tile
+      int pg_reg = 0;
       for (int i = 0; i < nt; ++i) {
         const int s = i % kStages;
-        if (i >= kStages && !mbar_wait(&kv_empty[s], ((i / kStages) - 1) & 1, p.err)) break;
-        mbar_arrive_expect_tx(&kv_full[s], S::kKVStage);
-        uint8_t* dst = sKV + s * S::kKVStage;
-        const int tok0 = k_lo + i * kTile;
-        for (int pg = 0; pg < 2; ++pg) {
-          const int lp = (tok0 + pg * kPage) / kPage;        // logical page (may be past the end: page 0)
-          const int page = (tok0 + pg * kPage < n) ? p.block_table[(int64_t)b * p.bt_stride + lp] : 0;
-          const int row = page * kPage;
-          for (int c = 0; c < 4; ++c)
-            tma_load_2d(dst + c * kTile * 128 + pg * kPage * 128, &tm_kv_lat, &kv_full[s], c * 128, row);
-          tma_load_2d(dst + S::kKVLat + pg * kPage * 64, &tm_kv_rope, &kv_full[s], kL, row);
+        if ((i & 15) == 0) {                         // 16 tiles = 32 pages per window
+          const int lp = lp0 + 2 * i + lane;
+          pg_reg = (lp * kPage < n) ? __ldcg(btr + lp) : 0;     // past the end: the scratch page 0
         }
+        int okw = 1;
+        if (lane == 0 && i >= kStages && !mbar_wait(&kv_empty[s], ((i / kStages) - 1) & 1, p.err)) okw = 0;
+        if (!__shfl_sync(0xffffffffu, okw, 0)) break;
+        const int pa = __shfl_sync(0xffffffffu, pg_reg, (2 * i) & 31);
+        const int pb = __shfl_sync(0xffffffffu, pg_reg, (2 * i + 1) & 31);
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&kv_full[s], S::kKVStage);
+          uint8_t* dst = sKV + s * S::kKVStage;
+          for (int pg = 0; pg < 2; ++pg) {
+            const int row = (pg ? pb : pa) * kPage;
+            for (int c = 0; c < 4; ++c)
+              tma_load_2d(dst + c * kTile * 128 + pg * kPage * 128, &tm_kv_lat, &kv_full[s], c * 128, row);
+            tma_load_2d(dst + S::kKVLat + pg * kPage * 64, &tm_kv_rope, &kv_full[s], kL, row);
+          }
+        }
+        __syncwarp();
       }
     }
   } else if (warp == 1) {
@@ -358,7 +395,7 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
       bool valid = tok0 + row < k_hi;
       if (SPARSE && valid) {
         const int pos = __ldcg(p.topk + (int64_t)t * p.topk_n + tok0 + row);
-        valid = pos >= 0 && pos < n;
+        valid = (pos >= 0 && pos < n) || (p.ratio2 > 0 && pos >= kMlaCompFlag);
       }
       float v[NC];
 #pragma unroll
@@ -641,6 +678,12 @@ static int launch(const MlaTcArgs& a, cudaStream_t st) {
   const int kv_box_rows = SPARSE ? 1 : kPage;
   if (map2d(&mkl, a.cache, a.cache_rows, kv_box_rows, 128, CU_TENSOR_MAP_SWIZZLE_128B)) return -4;
   if (map2d(&mkr, a.cache, a.cache_rows, kv_box_rows, 64, CU_TENSOR_MAP_SWIZZLE_64B)) return -5;
+  // compressed rows (sparse only; otherwise the maps repeat the main cache's, unused)
+  CUtensorMap mcl = mkl, mcr = mkr;
+  if (SPARSE && a.cache2 && a.ratio2 > 0) {
+    if (map2d(&mcl, a.cache2, a.cache2_rows, 1, 128, CU_TENSOR_MAP_SWIZZLE_128B)) return -7;
+    if (map2d(&mcr, a.cache2, a.cache2_rows, 1, 64, CU_TENSOR_MAP_SWIZZLE_64B)) return -8;
+  }
   Params p{};
   p.block_table = a.block_table;
   p.bt_stride = a.bt_stride;
@@ -660,10 +703,11 @@ static int launch(const MlaTcArgs& a, cudaStream_t st) {
   p.cache = a.cache;
   p.topk = a.topk;
   p.topk_n = a.topk_n;
+  p.ratio2 = (SPARSE && a.cache2) ? a.ratio2 : 0;
   auto kern = mla_tc_kernel<HB, SPARSE>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes);
   dim3 grid(a.T, a.H / HB, a.nsplit);
-  b200::launch_pdl(kern, dim3(grid), dim3(kThreads), S::kBytes, st, mql, mqr, mkl, mkr, p);
+  b200::launch_pdl(kern, dim3(grid), dim3(kThreads), S::kBytes, st, mql, mqr, mkl, mkr, mcl, mcr, p);
   if (cudaGetLastError() != cudaSuccess) return 1;
   if (a.nsplit > 1) {
     b200::launch_pdl(mla_merge_kernel, dim3(a.T * a.H), dim3(128), 0, st, a.part_o, a.part_lse, a.nsplit, a.T * a.H,

@@ -81,3 +81,12 @@ struct L2Regions {
   int n;
 };
 int b200_l2_prefetch(const L2Regions* r, int nctas, cudaStream_t st);
+
+// Compressed sparse attention (V4 family): store this step's gate logits g
+// (column of the qkv GEMM output, stride ld, bf16 or fp32) at their slots, then
+// write the compressed latent rows / indexer keys of the blocks of r
+// positions the step completes (kernels in v4.cu).
+int b200_compress_store(const void* g, int64_t ld, int gf32, const int64_t* slots, const int* pos, const int* q_seq,
+                        const int* bt, int bt_stride, int page, int r, int T, float* gate, const float* bias,
+                        const uint8_t* kv, int kvd, float kv_scale, const uint8_t* ik, const float* iks, int ikd,
+                        uint8_t* ckv, uint8_t* cik, float* cis, cudaStream_t st);

@@ -177,6 +177,122 @@ __global__ void __launch_bounds__(kThreads) ar_hc_post_kernel(int D, ArPeers pee
 }
 
 // ---------------------------------------------------------------------------
+// Compressed sparse attention: the compressor.
+//   gate_store     g[t] (the compressor's gate logit, a column of the qkv
+//                  GEMM output) -> gate[slot of row t].
+//   compress       one CTA per token row; rows whose position p completes a
+//                  block (p + 1 = 0 mod r) write block j = p / r: weights
+//                  softmax_k(gate[slot_k] + bias[k]) over its r positions, the
+//                  compressed latent row sum_k w_k kv[slot_k] (e4m3, the
+//                  cache's scale) and the compressed indexer key sum_k w_k
+//                  ik[slot_k] (e4m3 with its own scale amax / 448).  A block
+//                  lives in one page: its row is page * (page / r) + offset.
+// Separate launches: a block's other positions may be rows of the same step.
+__global__ void gate_store_kernel(const __nv_bfloat16* g, int64_t ld, int gf32, const int64_t* slots, int T,
+                                  float* gate) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  const float v = gf32 ? reinterpret_cast<const float*>(g)[(int64_t)t * ld] : __bfloat162float(g[(int64_t)t * ld]);
+  gate[slots[t]] = v;
+}
+
+__device__ __forceinline__ float e4m3_to_f(uint8_t b) {
+  __nv_fp8_e4m3 f;
+  f.__x = b;
+  return float(f);
+}
+
+__global__ void __launch_bounds__(128) compress_kernel(const int* pos, const int* q_seq, const int* bt, int bt_stride,
+                                                       int page, int r, const float* gate, const float* bias,
+                                                       const uint8_t* kv, int kvd, float kv_scale,
+                                                       const uint8_t* ik, const float* iks, int ikd, uint8_t* ckv,
+                                                       uint8_t* cik, float* cis) {
+  __shared__ float w_s[8];
+  __shared__ int64_t slot_s[8];
+  __shared__ float red[4];
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  const int t = blockIdx.x;
+  const int p = pos[t];
+  if ((p + 1) % r) return;                       // uniform per CTA
+  const int b = q_seq[t];
+  const int p0 = p + 1 - r;
+  if (threadIdx.x < r) {
+    const int q = p0 + threadIdx.x;
+    slot_s[threadIdx.x] = (int64_t)__ldcg(bt + (int64_t)b * bt_stride + q / page) * page + q % page;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m = -INFINITY;
+    float g[8];
+    for (int k = 0; k < r; ++k) {
+      g[k] = __ldcg(gate + slot_s[k]) + bias[k];
+      m = fmaxf(m, g[k]);
+    }
+    float sum = 0.f;
+    for (int k = 0; k < r; ++k) {
+      g[k] = __expf(g[k] - m);
+      sum += g[k];
+    }
+    for (int k = 0; k < r; ++k) w_s[k] = g[k] / sum;
+  }
+  __syncthreads();
+  const int cpage = page / r;
+  const int64_t crow = (int64_t)__ldcg(bt + (int64_t)b * bt_stride + p0 / page) * cpage + (p0 % page) / r;
+  // compressed latent row: 8 bytes per thread (the weighted mean keeps the cache's scale)
+  for (int c = threadIdx.x * 8; c < kvd; c += blockDim.x * 8) {
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    for (int k = 0; k < r; ++k) {
+      const uint2 raw = __ldcg(reinterpret_cast<const uint2*>(kv + slot_s[k] * kvd + c));
+      const uint8_t* bb = reinterpret_cast<const uint8_t*>(&raw);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = fmaf(w_s[k], e4m3_to_f(bb[i]), acc[i]);
+    }
+    uint2 outv;
+    uint16_t* o16 = reinterpret_cast<uint16_t*>(&outv);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o16[i] = f2_to_e4m3x2(acc[2 * i], acc[2 * i + 1]);
+    *reinterpret_cast<uint2*>(ckv + crow * kvd + c) = outv;
+  }
+  // compressed indexer key: 8 values per thread, one e4m3 scale per row
+  const int c = threadIdx.x * 8;
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  float amax = 0.f;
+  if (c < ikd) {
+    for (int k = 0; k < r; ++k) {
+      const float sk = __ldcg(iks + slot_s[k]) * w_s[k];
+      const uint2 raw = __ldcg(reinterpret_cast<const uint2*>(ik + slot_s[k] * ikd + c));
+      const uint8_t* bb = reinterpret_cast<const uint8_t*>(&raw);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = fmaf(sk, e4m3_to_f(bb[i]), acc[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(acc[i]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  amax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  const float sc = amax > 0.f ? amax / 448.f : 1.f;
+  const float inv = 1.f / sc;
+  if (c < ikd) {
+    uint2 outv;
+    uint16_t* o16 = reinterpret_cast<uint16_t*>(&outv);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o16[i] = f2_to_e4m3x2(acc[2 * i] * inv, acc[2 * i + 1] * inv);
+    *reinterpret_cast<uint2*>(cik + crow * ikd + c) = outv;
+  }
+  if (threadIdx.x == 0) cis[crow] = sc;
+}
+
+// ---------------------------------------------------------------------------
 // raw: row t holds `parts` partial mix vectors, part p at column p * pstride
 // (their sum is X_flat . fn^T).  mode 0: sublayer (pre / post / comb), mode 1:
 // head (pre only).  Outputs: post [T, 4], comb [T, 16] (mode 0); h as MXFP8
@@ -654,6 +770,19 @@ int b200_ar_hc_post(int T, int D, const ArPeers* peers, uint32_t* epoch, uint32_
   if (D % 8 || T > peers->max_t || peers->mc || expected <= 0) return -1;
   b200::launch_pdl(b200::v4::ar_hc_post_kernel, dim3(T), dim3(b200::v4::kThreads), 0, st, D, *peers, epoch, ticket,
                    (uint32_t)expected, reinterpret_cast<__nv_bfloat16*>(X), post, comb, sumsq, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : 1;
+}
+
+int b200_compress_store(const void* g, int64_t ld, int gf32, const int64_t* slots, const int* pos, const int* q_seq,
+                        const int* bt, int bt_stride, int page, int r, int T, float* gate, const float* bias,
+                        const uint8_t* kv, int kvd, float kv_scale, const uint8_t* ik, const float* iks, int ikd,
+                        uint8_t* ckv, uint8_t* cik, float* cis, cudaStream_t st) {
+  if (T <= 0) return 0;
+  if (r < 2 || r > 8 || page % r || kvd % 8 || ikd % 8 || ikd > 128 * 8) return -1;
+  b200::launch_pdl(b200::v4::gate_store_kernel, dim3((T + 127) / 128), dim3(128), 0, st,
+                   reinterpret_cast<const __nv_bfloat16*>(g), ld, gf32, slots, T, gate);
+  b200::launch_pdl(b200::v4::compress_kernel, dim3(T), dim3(128), 0, st, pos, q_seq, bt, bt_stride, page, r,
+                   (const float*)gate, bias, kv, kvd, kv_scale, ik, iks, ikd, ckv, cik, cis);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
 

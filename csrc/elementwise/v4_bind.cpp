@@ -142,6 +142,40 @@ void kv_store_v4(const at::Tensor& kv, const at::Tensor& w, double eps, const at
       "kv_store_v4");
 }
 
+// Compressed attention: gate logits of this step's rows to their slots, then
+// the compressed latent rows / indexer keys of the blocks the step completes.
+void compress_store(const at::Tensor& g, const at::Tensor& bias, const at::Tensor& pos, const at::Tensor& slots,
+                    const at::Tensor& q_seq, const at::Tensor& block_table, int64_t page, int64_t r,
+                    const at::Tensor& kv, double kv_scale, const at::Tensor& ik, const at::Tensor& iks, at::Tensor gate,
+                    at::Tensor ckv, at::Tensor cik, at::Tensor cis) {
+  TORCH_CHECK(g.is_cuda() && g.dim() == 1 && (g.scalar_type() == at::kBFloat16 || g.scalar_type() == at::kFloat),
+              "g bf16 / fp32 [T]");
+  TORCH_CHECK(bias.scalar_type() == at::kFloat && bias.is_contiguous() && bias.numel() == r, "bias fp32 [r]");
+  TORCH_CHECK(kv.dim() == 2 && kv.is_contiguous() && kv.element_size() == 1 && ckv.dim() == 2 &&
+                  ckv.is_contiguous() && ckv.element_size() == 1 && ckv.size(1) == kv.size(1),
+              "kv / ckv e4m3 rows of one width");
+  TORCH_CHECK(ik.dim() == 2 && ik.is_contiguous() && ik.element_size() == 1 && cik.dim() == 2 &&
+                  cik.is_contiguous() && cik.element_size() == 1 && cik.size(1) == ik.size(1),
+              "ik / cik e4m3 rows of one width");
+  TORCH_CHECK(iks.scalar_type() == at::kFloat && cis.scalar_type() == at::kFloat && gate.scalar_type() == at::kFloat &&
+                  gate.is_contiguous() && cis.is_contiguous(),
+              "scales / gate fp32");
+  TORCH_CHECK(ckv.size(0) * r >= kv.size(0) && cik.size(0) == ckv.size(0) && cis.numel() == ckv.size(0),
+              "compressed tensors hold one row per r slots");
+  TORCH_CHECK(pos.scalar_type() == at::kInt && q_seq.scalar_type() == at::kInt && slots.scalar_type() == at::kLong &&
+                  block_table.scalar_type() == at::kInt,
+              "int32 positions / sequences / block table, int64 slots");
+  const c10::cuda::CUDAGuard gd(g.device());
+  chk(b200_compress_store(g.data_ptr(), g.stride(0), g.scalar_type() == at::kFloat, slots.data_ptr<int64_t>(),
+                          pos.data_ptr<int>(), q_seq.data_ptr<int>(), block_table.data_ptr<int>(),
+                          block_table.stride(0), page, r, g.size(0), gate.data_ptr<float>(), bias.data_ptr<float>(),
+                          reinterpret_cast<const uint8_t*>(kv.data_ptr()), kv.size(1), float(kv_scale),
+                          reinterpret_cast<const uint8_t*>(ik.data_ptr()), iks.data_ptr<float>(), ik.size(1),
+                          reinterpret_cast<uint8_t*>(ckv.data_ptr()), reinterpret_cast<uint8_t*>(cik.data_ptr()),
+                          cis.data_ptr<float>(), cur()),
+      "compress_store");
+}
+
 void mqa_q_prep(const at::Tensor& q, const at::Tensor& pos, const at::Tensor& table, int64_t rd, at::Tensor q8,
                 at::Tensor qs) {
   TORCH_CHECK(q.is_cuda() && q.dim() == 3 && q.size(2) == 512 && q.stride(2) == 1 && q.scalar_type() == at::kBFloat16,
@@ -194,6 +228,7 @@ void register_v4(pybind11::module& m) {
   m.def("engram_gate", &engram_gate);
   m.def("kv_store_v4", &kv_store_v4);
   m.def("mqa_q_prep", &mqa_q_prep);
+  m.def("compress_store", &compress_store);
   m.def("attn_fixup", &attn_fixup);
   m.def("e5_prune", &e5_prune);
 }

@@ -155,6 +155,35 @@ def test_v4_sparse_indexer_with_window_matches_oracle():
     assert [o.token_ids for o in outs] == oracle.greedy(prompts, 5).tolist()
 
 
+def test_v4_compressed_sparse_attention_matches_oracle():
+    """Compressed sparse attention (ratio 2 on layer 1, ratio 4 on layer 2):
+    the compressor's gated block means, the indexer over compressed keys and
+    attention over the window + top compressed blocks follow the fp32 oracle
+    under chunked prefill (blocks completed across chunk boundaries) and
+    decode (blocks completed by decode tokens), and the prefix cache reuses
+    the compressed rows of cached pages."""
+    from b200ds import build_model_from
+    from b200ds.config import EngineConfig, tiny_v4_config
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.reference_v4 import ReferenceV4Model, init_weights_v4
+    cfg = tiny_v4_config(index_n_heads=8, index_head_dim=32, index_topk=6, index_swa=4, compress_ratios=(0, 2, 4),
+                         compress_topk=4)
+    assert [cfg.compress_ratio(i) for i in range(3)] == [0, 2, 4]
+    sd = init_weights_v4(cfg, 0)
+    prompts = _prompts(cfg, 2, 27, seed=9)
+    oracle = ReferenceV4Model(cfg, sd, 128)
+    want = oracle.greedy(prompts, 7).tolist()
+    for prefix in (False, True):
+        ecfg = EngineConfig(page_size=8, cuda_graphs=False, enable_prefix_cache=prefix, max_prefill_tokens=11)
+        eng = Engine(build_model_from(cfg, ecfg, sd, device="cpu"), ecfg)
+        outs = eng.generate(prompts.tolist(), SamplingParams(max_tokens=7))
+        assert [o.token_ids for o in outs] == want
+        if prefix:       # the same prompts again: full pages come from the prefix cache
+            again = eng.generate(prompts.tolist(), SamplingParams(max_tokens=7))
+            assert [o.token_ids for o in again] == want
+
+
 def _dp_rank(rank, world):
     from b200ds import build_model_from
     from b200ds.config import EngineConfig, tiny_v4_config

@@ -228,3 +228,86 @@ def test_small_v4_model_matches_oracle_and_graphs():
     torch.cuda.synchronize()
     assert all(len(o.token_ids) == 8 for o in outs)
     assert graphs.graphs is not None and len(graphs.graphs.graphs) == 1
+
+
+@pytest.mark.parametrize("r", [4, 2])
+def test_compressed_sparse_attention_kernels(r):
+    """Compressed sparse attention on the GPU against the fp32 references on
+    the same inputs: the compressor (gate logits to their slots, gated block
+    means of the e4m3 latent rows and indexer keys), the indexer over the
+    compressed keys (window + top blocks before it) and the sparse latent
+    attention gathering window rows from the cache and flagged blocks from
+    the compressed rows."""
+    from types import SimpleNamespace
+    from b200ds import ops
+    from b200ds.config import small_v4_gpu_config
+    from b200ds.models.rope import cos_sin_table
+    from b200ds.ops.ref import COMP_FLAG
+    torch.manual_seed(3)
+    cfg = small_v4_gpu_config()
+    L, rd, ps, NH, swa, topk = 512, 64, 64, 64, 64, 32
+    table = cos_sin_table(cfg, 4096, device=DEV)
+    lens = [1000, 300, 90]
+    B = len(lens)
+    pages = [(n + ps - 1) // ps for n in lens]
+    bt = torch.zeros(B, max(pages), dtype=torch.int32)
+    nxt = 1
+    for b, p in enumerate(pages):
+        bt[b, :p] = torch.arange(nxt, nxt + p, dtype=torch.int32).flip(0)     # pages out of order
+        nxt += p
+    slots_total = (nxt + 1) * ps
+    pos = torch.cat([torch.arange(n, dtype=torch.int32) for n in lens])
+    seq = torch.cat([torch.full((n,), b, dtype=torch.int32) for b, n in enumerate(lens)])
+    slots = bt[seq.long(), (pos // ps).long()].long() * ps + (pos % ps).long()
+    N = pos.numel()
+    cache = (torch.randn(slots_total, 576) * 0.5).to(torch.float8_e4m3fn)
+    cache[:, L:] = 0                      # the rope-key part stays zero (K = V = the latent row)
+    ik = (torch.randn(slots_total, 128) * 0.5).to(torch.float8_e4m3fn)
+    iks = torch.rand(slots_total) + 0.5
+    graw = torch.randn(N, 7).to(torch.bfloat16)
+    bias = torch.randn(r) * 0.5
+    nc = slots_total // r
+    # compressor: the whole prompt in one step
+    fb_all = SimpleNamespace(block_table=bt, q_seq=seq, positions=pos, out_slots=slots)
+    outs = {}
+    for dev in ("cpu", DEV):
+        f = SimpleNamespace(**{k: v.to(dev) for k, v in vars(fb_all).items()})
+        gate = torch.zeros(slots_total, device=dev)
+        ckv = torch.zeros(nc, 576, dtype=torch.float8_e4m3fn, device=dev)
+        cik = torch.zeros(nc, 128, dtype=torch.float8_e4m3fn, device=dev)
+        cis = torch.ones(nc, device=dev)
+        ops.compress_store(graw.to(dev)[:, 2], bias.to(dev), f, r, cache.to(dev), 0.7, ik.to(dev), iks.to(dev), gate,
+                           ckv, cik, cis, ps)
+        outs[dev] = [x.cpu() for x in (gate, ckv, cik, cis)]
+    (g0, kv0, ik0, s0), (g1, kv1, ik1, s1) = outs["cpu"], outs[DEV]
+    assert torch.equal(g0, g1)
+    assert rel_err(kv1.float(), kv0.float()) < 3e-2
+    assert rel_err(ik1.float() * s1.unsqueeze(-1), ik0.float() * s0.unsqueeze(-1)) < 3e-2
+    # decode-style queries at several positions of each sequence
+    qpos = torch.tensor([999, 640, 63, 299, 200, 89], dtype=torch.int32)
+    qseq = torch.tensor([0, 0, 0, 1, 1, 2], dtype=torch.int32)
+    T = qpos.numel()
+    fbq = SimpleNamespace(block_table=bt.to(DEV), q_seq=qseq.to(DEV), positions=qpos.to(DEV), is_decode=True,
+                          max_seq_len=max(lens), out_slots=None)
+    fbc = SimpleNamespace(block_table=bt, q_seq=qseq, positions=qpos)
+    q_raw = (torch.randn(T, NH * 128) * 0.3).to(torch.bfloat16)
+    w_raw = torch.randn(T, NH).to(torch.bfloat16)
+    sel = ops.indexer_topk_compressed(q_raw.to(DEV), w_raw.to(DEV), 0.01, table, ik1.to(DEV), s1.to(DEV),
+                                      fbq, ps, r, topk, swa).cpu()
+    want = ops.indexer_topk_compressed(q_raw, w_raw, 0.01, table.cpu(), ik1, s1, fbc, ps, r, topk, swa)
+    assert torch.equal(sel[:, :swa], want[:, :swa])
+    for t in range(T):
+        got = set(sel[t, swa:].tolist()) - {-1}
+        exp = set(want[t, swa:].tolist()) - {-1}
+        assert len(got) == len(exp) and all(e >= COMP_FLAG for e in got)
+        # e4m3 queries can swap near-tied blocks at the top-k boundary
+        assert len(got & exp) >= 0.85 * len(exp), (t, len(got & exp), len(exp))
+    # attention over the GPU selection, native vs reference
+    H = 16
+    q = (torch.randn(T, H, L) * 0.3).to(torch.bfloat16)
+    snk = torch.randn(H) * 2
+    o = ops.mqa_attention(q.to(DEV), cache.to(DEV), 0.7, fbq, cfg.softmax_scale, ps, snk.to(DEV), table, rd,
+                          sel.to(DEV), comp=(kv1.to(DEV), r))
+    exp = ops.mqa_attention(q.float(), cache, 0.7, fbc, cfg.softmax_scale, ps, snk, table.cpu(), rd, sel,
+                            comp=(kv1, r))
+    assert rel_err(o.cpu(), exp) < 3e-2, rel_err(o.cpu(), exp)
