@@ -668,7 +668,7 @@ def indexer_topk(q_raw, w_raw, w_factor, table, k_cache, k_scale, fb, page_size,
             j = torch.arange(cap, device=dev).unsqueeze(0)
             p = pos.long().unsqueeze(1)
             scores.masked_fill_((j > p - swa) & (j <= p), float("inf"))
-        _C.topk_select(scores, pos, out[t0:t1])
+        _C.topk_select(scores, pos, out[t0:t1], max_len)
     return out
 
 
@@ -705,7 +705,7 @@ def indexer_topk_compressed(q_raw, w_raw, w_factor, table, cik, cis, fb, page_si
         scores = torch.empty(n, cap, dtype=torch.float32, device=dev)
         _C.ix_score(q8, wq, ck, cis, fb.block_table, fb.q_seq[t0:t1], cpos[t0:t1], cpg, ix_splits(n, max_len),
                     scores)
-        _C.topk_select(scores, cpos[t0:t1], sel[t0:t1])
+        _C.topk_select(scores, cpos[t0:t1], sel[t0:t1], max_len)
     out[:, swa:] = torch.where(sel >= 0, sel + COMP_FLAG, torch.full_like(sel, -1))
     return out
 

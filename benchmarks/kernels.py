@@ -249,6 +249,19 @@ def run_indexer(B: int, ctx: int, iters: int):
     t = timed(fn, iters)
     report("indexer_topk", f"B={B} ctx={ctx} 64 heads x 128, top2048", t, nbytes=B * ctx * (128 + 4 + 4 * 2),
            flops=2 * B * ctx * 64 * 128, flop_peak=2 * BF16, note="q quant + tcgen05 scores + radix top-k")
+    # the two halves: tcgen05 scores alone, the top-k alone (one CTA per row / a cluster per row)
+    q8 = torch.empty(B * 64, 128, dtype=torch.uint8, device=dev)
+    wq = torch.empty(B, 64, dtype=torch.float32, device=dev)
+    _C.ix_q_quant(q, w, 64, 0.01, fb.positions, table, q8, wq)
+    scores = torch.empty(B, pages * ps, dtype=torch.float32, device=dev)
+    t_s = timed(lambda: _C.ix_score(q8, wq, kc, ks, bt, fb.q_seq, fb.positions, ps, cuda.ix_splits(B, ctx), scores),
+                iters)
+    report("ix_score", f"B={B} ctx={ctx} 64 heads x 128", t_s, nbytes=B * ctx * (128 + 4 + 4),
+           flops=2 * B * ctx * 64 * 128, flop_peak=2 * BF16)
+    out = torch.empty(B, 2048, dtype=torch.int32, device=dev)
+    for label, mx in (("one CTA per row", 0), ("cluster per row", ctx)):
+        t_k = timed(lambda: _C.topk_select(scores, fb.positions, out, mx), iters)
+        report("topk_select", f"B={B} n={ctx} top2048 {label}", t_k, nbytes=B * ctx * 4 + B * 2048 * 4)
 
 
 def run_gemm(name: str, T: int, N: int, K: int, iters: int):

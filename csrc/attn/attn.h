@@ -47,7 +47,10 @@ int b200_ix_q_quant(const void* q, int q_f32, int64_t ldq, const void* wraw, int
 int b200_ix_score(const uint8_t* q8, const float* wq, int T, int NH, const uint8_t* k_cache, int64_t cache_rows,
                   const float* k_scale, const int* block_table, int bt_stride, const int* q_seq, const int* q_pos,
                   int page_size, int nsplit, float* scores, int64_t ld, uint32_t* err, cudaStream_t st);
-int b200_topk_select(const float* scores, int64_t ld, const int* q_pos, int T, int K, int* out, cudaStream_t st);
+// max_n: the longest row (q_pos + 1) the caller knows of; above 8K the rows
+// are split over a cluster of CTAs (0: one CTA per row).
+int b200_topk_select(const float* scores, int64_t ld, const int* q_pos, int T, int K, int* out, cudaStream_t st,
+                     int max_n = 0);
 
 int b200_mla_q_quant(const void* q_abs, const void* q_pe, int TH, uint8_t* q8, float* qs, cudaStream_t st);
 // RoPE of the un-rotated q_pe + e4m3 quantization of [q_abs | q_pe] from

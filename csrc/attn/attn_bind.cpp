@@ -153,12 +153,12 @@ void ix_score(const at::Tensor& q8, const at::Tensor& wq, const at::Tensor& k_ca
   TORCH_CHECK(rc == 0, "ix_score failed ", rc);
 }
 
-void topk_select(const at::Tensor& scores, const at::Tensor& q_pos, at::Tensor out) {
+void topk_select(const at::Tensor& scores, const at::Tensor& q_pos, at::Tensor out, int64_t max_n) {
   TORCH_CHECK(scores.is_cuda() && scores.scalar_type() == at::kFloat && scores.stride(1) == 1, "scores fp32");
   TORCH_CHECK(out.scalar_type() == at::kInt && out.is_contiguous() && out.dim() == 2, "out int32 [T, K]");
   const c10::cuda::CUDAGuard g(scores.device());
   const int rc = b200_topk_select(scores.data_ptr<float>(), scores.stride(0), q_pos.data_ptr<int>(), out.size(0),
-                                  out.size(1), out.data_ptr<int>(), cur());
+                                  out.size(1), out.data_ptr<int>(), cur(), int(max_n));
   TORCH_CHECK(rc == 0, "topk_select failed ", rc);
 }
 
@@ -176,5 +176,6 @@ void register_attn(pybind11::module& m) {
   m.def("ix_k_store", &ix_k_store);
   m.def("ix_q_quant", &ix_q_quant);
   m.def("ix_score", &ix_score);
-  m.def("topk_select", &topk_select);
+  m.def("topk_select", &topk_select, pybind11::arg("scores"), pybind11::arg("q_pos"), pybind11::arg("out"),
+        pybind11::arg("max_n") = 0);
 }

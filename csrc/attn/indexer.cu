@@ -27,6 +27,8 @@
 // serving fork's top-k (ix.py:5-18, ct.py:8-14); these kernels are our own.
 #include "../common/ptx.cuh"
 #include "../common/radix_select.cuh"
+#include <algorithm>
+
 #include "attn.h"
 
 namespace b200 {
@@ -289,6 +291,40 @@ topk_select_kernel(const float* scores, int64_t ld, const int* q_pos, int K, int
   rsel::select_topk([&](int i) { return __ldcg(sc + i); }, n, K, sm, [&](int slot, int i) { o[slot] = i; });
 }
 
+// Cluster variant: grid (C, T), one cluster of C CTAs per row; each CTA
+// stages its slice of at most `cap` scores as order keys in shared memory.
+// Rows longer than C * cap (a bound the host sized from the longest row it
+// knows of) fall back to the one-CTA select over global memory.
+__global__ void __launch_bounds__(kTopkThreads)
+topk_cluster_kernel(const float* scores, int64_t ld, const int* q_pos, int K, int C, int cap, int* out) {
+  extern __shared__ __align__(16) uint32_t keys[];
+  __shared__ rsel::ClusterSmem sm;
+  __shared__ rsel::Smem sm1;
+  const int t = blockIdx.y;
+  const int rank = int(cluster_ctarank());
+  pdl_wait();
+  pdl_launch_dependents();
+  const int n = q_pos[t] + 1;          // uniform over the cluster: early exits skip no barrier
+  int* o = out + (int64_t)t * K;
+  const float* sc = scores + (int64_t)t * ld;
+  if (n <= K) {
+    if (rank == 0)
+      for (int i = threadIdx.x; i < K; i += kTopkThreads) o[i] = i < n ? i : -1;
+    return;
+  }
+  const int chunk = (n + C - 1) / C;
+  if (chunk > cap) {
+    if (rank == 0)
+      rsel::select_topk([&](int i) { return __ldcg(sc + i); }, n, K, sm1, [&](int slot, int i) { o[slot] = i; });
+    return;
+  }
+  const int lo = rank * chunk;
+  const int m = max(0, min(n, lo + chunk) - lo);
+  for (int i = threadIdx.x; i < m; i += kTopkThreads) keys[i] = rsel::order_key(__ldcg(sc + lo + i));
+  __syncthreads();
+  rsel::cluster_select_topk(keys, m, lo, K, C, rank, sm, [&](int slot, int i) { o[slot] = i; });
+}
+
 // ----------------------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -368,10 +404,36 @@ int b200_ix_score(const uint8_t* q8, const float* wq, int T, int NH, const uint8
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
 
-int b200_topk_select(const float* scores, int64_t ld, const int* q_pos, int T, int K, int* out, cudaStream_t st) {
+int b200_topk_select(const float* scores, int64_t ld, const int* q_pos, int T, int K, int* out, cudaStream_t st,
+                     int max_n) {
   if (T <= 0) return 0;
   if (K <= 0) return -1;
-  b200::launch_pdl(b200::ix::topk_select_kernel, dim3(T), dim3(b200::ix::kTopkThreads), 0, st, scores, ld, q_pos, K,
-                   out);
-  return cudaGetLastError() == cudaSuccess ? 0 : 1;
+  // cluster of C CTAs per row, about 4K scores (16 KB of keys) each
+  constexpr int kMaxC = 8, kPerCta = 4096, kMaxSmem = 200 * 1024;
+  const int C = std::min(kMaxC, std::max(1, (max_n + kPerCta - 1) / kPerCta));
+  const int cap = ((max_n + C - 1) / C + 3) & ~3;
+  if (max_n <= K || C < 2 || cap * 4 > kMaxSmem) {
+    b200::launch_pdl(b200::ix::topk_select_kernel, dim3(T), dim3(b200::ix::kTopkThreads), 0, st, scores, ld, q_pos,
+                     K, out);
+    return cudaGetLastError() == cudaSuccess ? 0 : 1;
+  }
+  auto kern = b200::ix::topk_cluster_kernel;
+  const size_t smem = size_t(cap) * 4;
+  if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(C, T);
+  cfg.blockDim = dim3(b200::ix::kTopkThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = b200::pdl_enabled() ? 2 : 1;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kern, scores, ld, q_pos, K, C, cap, out);
+  return err == cudaSuccess ? 0 : 1000 + int(err);
 }

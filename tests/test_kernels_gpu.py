@@ -358,6 +358,34 @@ def test_ix_score_and_topk(lens, decode):
         assert (out[t, kk:] == -1).all()
 
 
+@pytest.mark.parametrize("ties", [False, True])
+def test_topk_select_cluster_matches_single_cta(ties):
+    """The cluster top-k (a row split over up to 8 CTAs, digit histograms
+    summed through distributed shared memory) returns exactly the one-CTA
+    select's positions: ascending, ties taken lowest index first, -1 padded
+    for short rows, and the one-CTA fallback for rows longer than the bound."""
+    from b200ds import _C
+    torch.manual_seed(5)
+    lens = [1, 2048, 2049, 5000, 33000, 70000, 131072, 9000]
+    T, K, cap = len(lens), 2048, 131072
+    scores = torch.randn(T, cap, device=DEV)
+    if ties:
+        scores = (scores * 4).round() / 4          # a few dozen distinct values
+    pos = torch.tensor([n - 1 for n in lens], dtype=torch.int32, device=DEV)
+    one = torch.empty(T, K, dtype=torch.int32, device=DEV)
+    _C.topk_select(scores, pos, one)
+    for max_n in (max(lens), 40000):               # 40000: the longer rows take the fallback
+        many = torch.full((T, K), -7, dtype=torch.int32, device=DEV)
+        _C.topk_select(scores, pos, many, max_n)
+        assert torch.equal(many, one), max_n
+    for t, n in enumerate(lens):
+        kk = min(K, n)
+        got = one[t, :kk].long().cpu()
+        assert (got[1:] > got[:-1]).all()
+        thr = scores[t, :n].topk(kk).values[-1].item()
+        assert (scores[t].cpu()[got] >= thr).all()
+
+
 @pytest.mark.parametrize("H,lens", [(16, [3000, 40, 2100]), (128, [5000]), (32, [2048, 2049])])
 def test_mla_tc_sparse_matches_reference(H, lens):
     from types import SimpleNamespace
