@@ -321,9 +321,13 @@ class DeepseekV4Model:
         carry = None
         for i, lw in enumerate(self.layers):
             tr.mark(f"L{i}.attn")
-            if carry is not None:
+            tail = i == c.late_layer_start and fb.tail_from is not None
+            if carry is not None and (tail or lw.engram is not None or isinstance(carry[0], _Partial)):
+                # the post runs on its own where something acts on X before
+                # the coefficients (or fused with the TP all-reduce)
                 ss = self._post(X, *carry)
-            if i == c.late_layer_start and fb.tail_from is not None:
+                carry = None
+            if tail:
                 # prefill tail: the window-only layers need only the rows within
                 # reach of each prompt's end (ForwardBatch.tail_rows)
                 rows = fb.tail_rows()
@@ -333,19 +337,25 @@ class DeepseekV4Model:
                 fb = fb.take_rows(rows)
             if lw.engram is not None:
                 ss = ops.engram_update(X, eids, lw.engram, c, self.ps)
+            # hc_post of the previous FFN + the attention coefficients + its input
+            h, post, comb = ops.hc_boundary(X, carry, lw.attn_hc, lw.in_ln, eps, c, lw.attn.wqkv_a, sumsq=ss)
             if i in c.aux_layers:
                 self.aux.append(ops.hc_mean(X))
-            h, post, comb = ops.hc_pre(X, ss, lw.attn_hc, lw.in_ln, eps, c, lw.attn.wqkv_a)
             y = self._attention(i, lw, h, fb)
-            ss = self._post(X, y, post, comb)
+            carry, ss = (y, post, comb), None
+            if isinstance(y, _Partial):
+                ss = self._post(X, *carry)
+                carry = None
             tr.mark(f"L{i}.ffn")
             moe = isinstance(lw.ffn, MoEWeights)
-            h, post, comb = ops.hc_pre(X, ss, lw.ffn_hc, lw.post_ln, eps, c, self._ffn_first_linear(lw),
-                                       keep_hf=moe)
-            carry = (self._ffn(i, lw, h, fb), post, comb)
+            h, post, comb = ops.hc_boundary(X, carry, lw.ffn_hc, lw.post_ln, eps, c, self._ffn_first_linear(lw),
+                                            keep_hf=moe, sumsq=ss)
+            carry, ss = (self._ffn(i, lw, h, fb), post, comb), None
         tr.mark("head")
-        ss = self._post(X, *carry)
-        h, _, _ = ops.hc_pre(X, ss, self.hc_head, self.final_ln, eps, c, None, head=True)
+        if isinstance(carry[0], _Partial):
+            ss = self._post(X, *carry)
+            carry = None
+        h, _, _ = ops.hc_boundary(X, carry, self.hc_head, self.final_ln, eps, c, None, head=True, sumsq=ss)
         return h, fb
 
     def _last_hidden(self, h, fb: ForwardBatch) -> torch.Tensor:

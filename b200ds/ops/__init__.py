@@ -546,6 +546,19 @@ def hc_pre(X: torch.Tensor, sumsq: torch.Tensor, hw: HcWeights, norm_w: torch.Te
     return rmsnorm_act(x, norm_w, eps, next_linear, keep_hf), post, comb
 
 
+def hc_boundary(X: torch.Tensor, carry, hw: HcWeights, norm_w: torch.Tensor, eps: float, cfg, next_linear=None,
+                head: bool = False, keep_hf: bool = False, sumsq: Optional[torch.Tensor] = None):
+    """A whole hyper-connection boundary: hc_post of the previous sublayer's
+    output carry = (y, post, comb) into X (None: X is already up to date and
+    sumsq holds its row sums of squares), then hc_pre.  Returns (h, post,
+    comb) like hc_pre.  On GPUs decode-sized batches run it as one kernel."""
+    if _use_native(X) and _native().hc_boundary_ok(X):
+        return _native().hc_boundary(X, carry, hw, norm_w, eps, cfg, next_linear, head, keep_hf)
+    if carry is not None:
+        sumsq = hc_post(X, *carry)
+    return hc_pre(X, sumsq, hw, norm_w, eps, cfg, next_linear, head=head, keep_hf=keep_hf)
+
+
 def hc_mean(X: torch.Tensor) -> torch.Tensor:
     if _use_native(X):
         return _native().hc_mean(X)

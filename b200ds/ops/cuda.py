@@ -833,6 +833,38 @@ def hc_pre(X, sumsq, hw, norm_w, eps, cfg, next_linear, head, keep_hf):
     return hb, post, comb
 
 
+HC_BOUNDARY_MAX_T = 256      # above: the tcgen05 stats GEMM (fn read once per 128 rows)
+
+
+def hc_boundary_ok(X) -> bool:
+    T, hc, D = X.shape
+    return levers.on("hc_boundary") and T <= HC_BOUNDARY_MAX_T and hc == 4 and D % 256 == 0
+
+
+def hc_boundary(X, carry, hw, norm_w, eps, cfg, next_linear, head, keep_hf):
+    """One kernel for the boundary: hc_post of carry = (y, post, comb) (None:
+    X is up to date), the mixes in fp32, the coefficients and the normed
+    sublayer input, a cluster of CTAs per row."""
+    T, hc, D = X.shape
+    y = post_in = comb_in = None
+    if carry is not None:
+        y, post_in, comb_in = carry
+        y = y if y.dtype == torch.bfloat16 else y.to(torch.bfloat16)
+    quantized = next_linear is not None and getattr(next_linear, "quantized", False)
+    post = comb = None
+    if not head:
+        post = torch.empty(T, hc, dtype=torch.float32, device=X.device)
+        comb = torch.empty(T, hc * hc, dtype=torch.float32, device=X.device)
+    a = alloc_qact(T, D, X.device) if quantized else None
+    hb = torch.empty(T, D, dtype=torch.bfloat16, device=X.device) if (keep_hf or not quantized) else None
+    _C.hc_boundary(X, y, post_in, comb_in, hw.fn, hw.scale, hw.base, 1 if head else 0, cfg.hc_sinkhorn_iters,
+                   cfg.hc_eps, norm_w, eps, post, comb, a.q if a else None, a.sf if a else None, hb, None)
+    if a is not None:
+        a.hf = hb
+        return a, post, comb
+    return hb, post, comb
+
+
 def hc_mean(X):
     out = torch.empty(X.shape[0], X.shape[2], dtype=torch.bfloat16, device=X.device)
     _C.hc_mean(X, out)

@@ -1,0 +1,98 @@
+"""Prefill cost of the DeepSeek-V3-shaped decoder on one GPU, per layer kind.
+
+Builds a model of the flagship's widths with few layers (one dense layer and
+`--moe-layers` MoE layers, random-init MXFP8 weights), runs a batch prefill
+of `--batch` prompts x `--input-len` tokens through the engine (the same
+chunked path `bench.py` times as TTFT), once cold and then `--iters` times
+warm, and prints JSON lines: the cold and warm wall times on the device (CUDA
+events) and the warm time per layer, and, with
+`--kernels`, the warm chunk's device time per kernel name from the PyTorch
+profiler (shares only: numbers under a profiler are not timings).
+
+    python benchmarks/prefill.py --batch 16 --input-len 1024 --moe-layers 3 --kernels
+"""
+import argparse
+import json
+import os
+import sys
+
+import torch
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--batch", type=int, default=16)
+    ap.add_argument("--input-len", type=int, default=1024)
+    ap.add_argument("--moe-layers", type=int, default=3)
+    ap.add_argument("--chunk", type=int, default=16384)
+    ap.add_argument("--iters", type=int, default=2)
+    ap.add_argument("--kernels", action="store_true")
+    a = ap.parse_args()
+
+    from b200ds import ops
+    from b200ds.config import EngineConfig, v3_671b_config
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.random_init import build_random_model
+    from b200ds.parallel.state import init_parallel
+    import b200ds._C  # noqa: F401
+
+    ops.set_impl("native")
+    ps = init_parallel(backend="nccl", timeout_s=300)
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = v3_671b_config(num_hidden_layers=1 + a.moe_layers, first_k_dense_replace=1)
+    ctx = a.input_len + 8
+    pages = (ctx + 63) // 64
+    n_req = a.batch * (2 + a.iters)
+    ecfg = EngineConfig(page_size=64, max_num_seqs=a.batch, max_prefill_tokens=a.chunk, cuda_graphs=False,
+                        enable_prefix_cache=False, max_model_len=ctx + 64)
+    model = build_random_model(cfg, ecfg, ps, dev, seed=0, reserve_bytes=8e9 + n_req * ctx * 700 * cfg.num_hidden_layers)
+    eng = Engine(model, ecfg, num_pages=a.batch * pages + 8)
+    g = torch.Generator().manual_seed(0)
+
+    def one_batch():
+        prompts = torch.randint(0, cfg.vocab_size, (a.batch, a.input_len), generator=g).tolist()
+        reqs = [eng.add_request(p, SamplingParams(max_tokens=1, ignore_eos=True)) for p in prompts]
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        while any(r.t_first is None for r in reqs):
+            eng.step()
+        e1.record()
+        torch.cuda.synchronize()
+        while any(not r.finished for r in reqs):
+            eng.step()
+        return e0.elapsed_time(e1)
+
+    cold = one_batch()
+    warm = [one_batch() for _ in range(a.iters)]
+    w = min(warm)
+    tokens = a.batch * a.input_len
+    print(json.dumps({"bench": "prefill", "batch": a.batch, "input_len": a.input_len, "layers": cfg.num_hidden_layers,
+                      "moe_layers": a.moe_layers, "chunk": a.chunk, "cold_ms": round(cold, 2),
+                      "warm_ms": round(w, 2), "warm_all_ms": [round(x, 2) for x in warm],
+                      "tokens": tokens, "warm_tok_s": round(tokens / w * 1e3, 1),
+                      "warm_ms_per_layer": round(w / cfg.num_hidden_layers, 2)}), flush=True)
+    if a.kernels:
+        from torch.profiler import ProfilerActivity, profile
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            one_batch()
+        rows = []
+        for ev in prof.key_averages():
+            dt = getattr(ev, "device_time_total", None)
+            if dt is None:
+                dt = getattr(ev, "cuda_time_total", 0)
+            if dt and ev.count:
+                rows.append((dt, ev.count, ev.key))
+        rows.sort(reverse=True)
+        total = sum(r[0] for r in rows) or 1.0
+        for dt, cnt, key in rows[:40]:
+            print(json.dumps({"kernel": key[:120], "device_us": round(dt, 1), "calls": cnt,
+                              "share": round(dt / total, 4)}), flush=True)
+
+
+if __name__ == "__main__":
+    main()

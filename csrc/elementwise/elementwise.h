@@ -52,6 +52,13 @@ int b200_hc_pre(const float* raw, int ldr, int parts, int pstride, const float* 
                 const float* base, int mode, int iters, float eps, float inv_width, const void* X, int T, int hc,
                 int D, const float* norm_w, float norm_eps, float* post, float* comb, uint8_t* q, uint8_t* sf,
                 void* hb, float* hf, cudaStream_t st);
+// Fused hyper-connection boundary (hc_post when y is set, fp32 mixes, the
+// coefficients, the normed sublayer input) of T rows; a row per cluster of
+// CTAs.  mode 0 needs M = 24 (pre, post, comb), mode 1 (head) M = 4.
+int b200_hc_boundary(void* X, int T, int hc, int D, const void* y, int64_t ldy, const float* post_in,
+                     const float* comb_in, const float* fn, int M, const float* scale, const float* base, int mode,
+                     int iters, float eps, float inv_width, const float* norm_w, float norm_eps, float* post,
+                     float* comb, uint8_t* q, uint8_t* sf, void* hb, float* hf, cudaStream_t st);
 int b200_hc_mean(const void* X, int T, int hc, int D, void* out, cudaStream_t st);
 int b200_engram_hash(const int* ids, const int* pos, const int* q_seq, const int* block_table, int bt_stride,
                      const int64_t* out_slots, int page_size, int* tok_cache, int T, int heads, int per_head,

@@ -293,6 +293,46 @@ __global__ void __launch_bounds__(128) compress_kernel(const int* pos, const int
 }
 
 // ---------------------------------------------------------------------------
+// Coefficients of one row from its raw mixes (mix(j) = X_flat . fn[j]), run
+// by the 32 lanes of one warp: sigmoid pre -> pre_s[4]; mode 0 also
+// 2*sigmoid post -> post_row[4] and the row-softmax + Sinkhorn comb on 16
+// lanes (mirrored on lanes 16-31) -> comb_row[16] (written when the row
+// pointers are non-null).
+template <class Mix>
+__device__ __forceinline__ void hc_coeffs_warp(Mix mix, float rs, const float* scale, const float* base, int mode,
+                                               int iters, float eps, float* pre_s, float* post_row,
+                                               float* comb_row) {
+  const int l = threadIdx.x & 15;
+  if (l < kHC) {
+    const float pre = sigmoidf(scale[0] * rs * mix(l) + base[l]) + eps;
+    if (threadIdx.x < kHC) pre_s[l] = pre;
+    if (mode == 0 && threadIdx.x < kHC && post_row)
+      post_row[l] = 2.f * sigmoidf(scale[1] * rs * mix(kHC + l) + base[kHC + l]);
+  }
+  if (mode == 0) {
+    // lane l: comb[r][c], r = l / 4, c = l % 4; row peers differ in lane
+    // bits 0-1, column peers in bits 2-3
+    float m = scale[2] * rs * mix(2 * kHC + l) + base[2 * kHC + l];
+    float mx = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    m = expf(m - mx);
+    float s = m + __shfl_xor_sync(0xffffffffu, m, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    m = m / s + eps;
+    for (int it = 0; it < iters; ++it) {
+      if (it > 0) {
+        float rsum = m + __shfl_xor_sync(0xffffffffu, m, 1);
+        rsum += __shfl_xor_sync(0xffffffffu, rsum, 2);
+        m = m / (rsum + eps);
+      }
+      float csum = m + __shfl_xor_sync(0xffffffffu, m, 4);
+      csum += __shfl_xor_sync(0xffffffffu, csum, 8);
+      m = m / (csum + eps);
+    }
+    if (threadIdx.x < 16 && comb_row) comb_row[l] = m;
+  }
+}
+
 // raw: row t holds `parts` partial mix vectors, part p at column p * pstride
 // (their sum is X_flat . fn^T).  mode 0: sublayer (pre / post / comb), mode 1:
 // head (pre only).  Outputs: post [T, 4], comb [T, 16] (mode 0); h as MXFP8
@@ -309,42 +349,14 @@ __global__ void __launch_bounds__(kThreads) hc_pre_kernel(const float* raw, int 
   if (threadIdx.x == 0) pdl_launch_dependents();
   const int t = blockIdx.x;
   if (threadIdx.x < 32) {
-    const int l = threadIdx.x & 15;
     const float rs = 1.f / sqrtf(__ldcg(sumsq + t) * inv_width + eps);
     auto mix = [&](int j) {
       float a = 0.f;
       for (int p = 0; p < parts; ++p) a += __ldcg(raw + (int64_t)t * ldr + p * pstride + j);
       return a;
     };
-    if (l < kHC) {
-      const float pre = sigmoidf(scale[0] * rs * mix(l) + base[l]) + eps;
-      if (threadIdx.x < kHC) pre_s[l] = pre;
-      if (mode == 0 && threadIdx.x < kHC) {
-        post_out[(int64_t)t * kHC + l] = 2.f * sigmoidf(scale[1] * rs * mix(kHC + l) + base[kHC + l]);
-      }
-    }
-    if (mode == 0) {
-      // lane l (mirrored on lanes 16-31): comb[r][c], r = l / 4, c = l % 4;
-      // row peers differ in lane bits 0-1, column peers in bits 2-3
-      float m = scale[2] * rs * mix(2 * kHC + l) + base[2 * kHC + l];
-      float mx = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      m = expf(m - mx);
-      float s = m + __shfl_xor_sync(0xffffffffu, m, 1);
-      s += __shfl_xor_sync(0xffffffffu, s, 2);
-      m = m / s + eps;
-      for (int it = 0; it < iters; ++it) {
-        if (it > 0) {
-          float rsum = m + __shfl_xor_sync(0xffffffffu, m, 1);
-          rsum += __shfl_xor_sync(0xffffffffu, rsum, 2);
-          m = m / (rsum + eps);
-        }
-        float csum = m + __shfl_xor_sync(0xffffffffu, m, 4);
-        csum += __shfl_xor_sync(0xffffffffu, csum, 8);
-        m = m / (csum + eps);
-      }
-      if (threadIdx.x < 16) comb_out[(int64_t)t * kHC * kHC + l] = m;
-    }
+    hc_coeffs_warp(mix, rs, scale, base, mode, iters, eps, pre_s, mode == 0 ? post_out + (int64_t)t * kHC : nullptr,
+                   mode == 0 ? comb_out + (int64_t)t * kHC * kHC : nullptr);
   }
   __syncthreads();
   float p[kHC];
@@ -384,6 +396,197 @@ __global__ void __launch_bounds__(kThreads) hc_pre_kernel(const float* raw, int 
     if (hb) store8_bf16(hb + (int64_t)t * D + v, y);
     if (hf) store8_f32(hf + (int64_t)t * D + v, y);
     if (q) quant8(y, q + (int64_t)t * D + v, sf, t, v, kb, true);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// The whole hyper-connection boundary of one row in one kernel: hc_post of
+// the previous sublayer's output (when y is given), the raw mixes
+// X_flat . fn^T in fp32 on the CUDA cores, the coefficients, and the next
+// sublayer's input RMSNorm(sum_c pre_c X_c) * w.  A row is split over the C
+// CTAs of a thread-block cluster, CTA r owning columns [r D/C, (r+1) D/C) of
+// every stream; the C partial mixes (and sums of squares) are summed in rank
+// order through distributed shared memory, so every CTA computes the same
+// coefficients.  Decode-sized batches: every row reads all of fn (M x 4D
+// fp32, from L2); long prefill chunks keep the tcgen05 stats GEMM.
+// Replaces hc_post + memset + stats GEMM + hc_pre (four launches).
+constexpr int kBThreads = 128;
+constexpr int kBMaxM = 24;
+
+__global__ void __launch_bounds__(kBThreads) hc_boundary_kernel(
+    __nv_bfloat16* X, int D, int C, const __nv_bfloat16* y, int64_t ldy, const float* post_in, const float* comb_in,
+    const float* fn, int M, const float* scale, const float* base, int mode, int iters, float eps, float inv_width,
+    const float* norm_w, float norm_eps, float* post_out, float* comb_out, uint8_t* q, uint8_t* sf,
+    __nv_bfloat16* hb, float* hf) {
+  extern __shared__ __align__(16) float xs[];       // [kHC][Dq] this CTA's columns of the updated streams
+  __shared__ float part[kBMaxM + 2];                // raw mixes [M], sum sq of X, sum sq of h
+  __shared__ float wsum[kBThreads / 32][kBMaxM + 1];
+  __shared__ float tot[kBMaxM + 1];
+  __shared__ float cf[kHC * kHC + kHC];
+  __shared__ float pre_s[kHC];
+  __shared__ float red[32];
+  const int t = blockIdx.y;
+  const int rank = int(cluster_ctarank());
+  const int Dq = D / C, d0 = rank * Dq;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nit = (Dq + kBThreads * 8 - 1) / (kBThreads * 8);
+  pdl_wait();
+  if (tid == 0) pdl_launch_dependents();
+  if (y) {
+    if (tid < kHC * kHC) cf[tid] = __ldcg(comb_in + (int64_t)t * kHC * kHC + tid);
+    if (tid < kHC) cf[kHC * kHC + tid] = __ldcg(post_in + (int64_t)t * kHC + tid);
+    __syncthreads();
+  }
+  __nv_bfloat16* xt = X + (int64_t)t * kHC * D + d0;
+  // 1. hc_post on this CTA's columns (in place), streams kept in fp32 smem
+  float ssx = 0.f;
+  for (int it = 0; it < nit; ++it) {
+    const int v = (tid + it * kBThreads) * 8;
+    if (v >= Dq) break;
+    float xr[kHC][8];
+#pragma unroll
+    for (int r = 0; r < kHC; ++r) load8(xt + (int64_t)r * D + v, xr[r]);
+    if (y) {
+      float yv[8];
+      load8(y + (int64_t)t * ldy + d0 + v, yv);
+      float o[kHC][8];
+#pragma unroll
+      for (int c = 0; c < kHC; ++c) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float a = cf[kHC * kHC + c] * yv[i];
+#pragma unroll
+          for (int r = 0; r < kHC; ++r) a = fmaf(cf[r * kHC + c], xr[r][i], a);
+          o[c][i] = bf16_round(a);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < kHC; ++c) {
+        store8_bf16(xt + (int64_t)c * D + v, o[c]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) xr[c][i] = o[c][i];
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < kHC; ++c) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        xs[c * Dq + v + i] = xr[c][i];
+        ssx = fmaf(xr[c][i], xr[c][i], ssx);
+      }
+    }
+  }
+  // 2. partial raw mixes over this CTA's columns: fn row m, column c D + d
+  float acc[kBMaxM];
+#pragma unroll
+  for (int m = 0; m < kBMaxM; ++m) acc[m] = 0.f;
+  const int64_t K = (int64_t)kHC * D;
+  for (int it = 0; it < nit; ++it) {
+    const int v = (tid + it * kBThreads) * 8;
+    if (v >= Dq) break;
+#pragma unroll
+    for (int c = 0; c < kHC; ++c) {
+      float xv[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) xv[i] = xs[c * Dq + v + i];
+      const float* f = fn + (int64_t)c * D + d0 + v;
+#pragma unroll
+      for (int m = 0; m < kBMaxM; ++m) {
+        if (m < M) {
+          const float4 a = __ldg(reinterpret_cast<const float4*>(f + m * K));
+          const float4 b = __ldg(reinterpret_cast<const float4*>(f + m * K + 4));
+          acc[m] = fmaf(xv[0], a.x, fmaf(xv[1], a.y, fmaf(xv[2], a.z, fmaf(xv[3], a.w, acc[m]))));
+          acc[m] = fmaf(xv[4], b.x, fmaf(xv[5], b.y, fmaf(xv[6], b.z, fmaf(xv[7], b.w, acc[m]))));
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < kBMaxM; ++m) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ssx += __shfl_xor_sync(0xffffffffu, ssx, o);
+  if (lane == 0) {
+#pragma unroll
+    for (int m = 0; m < kBMaxM; ++m) wsum[warp][m] = acc[m];
+    wsum[warp][kBMaxM] = ssx;
+  }
+  __syncthreads();
+  if (tid <= kBMaxM) {
+    float a = 0.f;
+#pragma unroll
+    for (int w = 0; w < kBThreads / 32; ++w) a += wsum[w][tid];
+    part[tid] = a;
+  }
+  // 3. the cluster's partials, summed in rank order (the same in every CTA)
+  cluster_sync();
+  if (tid <= kBMaxM) {
+    const uint32_t a = smem_u32(&part[tid]);
+    float s = 0.f;
+    for (int r = 0; r < C; ++r) s += ld_dsmem_f32(mapa_shared(a, r));
+    tot[tid] = s;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const float rs = 1.f / sqrtf(tot[kBMaxM] * inv_width + eps);
+    const bool w0 = rank == 0 && mode == 0;
+    hc_coeffs_warp([&](int j) { return tot[j]; }, rs, scale, base, mode, iters, eps, pre_s,
+                   w0 ? post_out + (int64_t)t * kHC : nullptr, w0 ? comb_out + (int64_t)t * kHC * kHC : nullptr);
+  }
+  __syncthreads();
+  // 4. h = sum_c pre_c X_c on this CTA's columns; its sum of squares over the cluster
+  float p[kHC];
+#pragma unroll
+  for (int c = 0; c < kHC; ++c) p[c] = pre_s[c];
+  float ssh = 0.f;
+  for (int it = 0; it < nit; ++it) {
+    const int v = (tid + it * kBThreads) * 8;
+    if (v >= Dq) break;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float h = 0.f;
+#pragma unroll
+      for (int c = 0; c < kHC; ++c) h = fmaf(p[c], xs[c * Dq + v + i], h);
+      ssh = fmaf(h, h, ssh);
+    }
+  }
+  ssh = block_sum(ssh, red);
+  if (tid == 0) part[kBMaxM + 1] = ssh;
+  cluster_sync();
+  if (tid == 0) {
+    const uint32_t a = smem_u32(&part[kBMaxM + 1]);
+    float s = 0.f;
+    for (int r = 0; r < C; ++r) s += ld_dsmem_f32(mapa_shared(a, r));
+    red[0] = s;
+  }
+  // the last reads of other CTAs' shared memory are done after this barrier
+  cluster_sync();
+  const float rstd = 1.f / sqrtf(red[0] / D + norm_eps);
+  const int kb = D / 32;
+  // 5. RMSNorm * w -> bf16 / fp32 / MXFP8 (a uniform trip count: quant8's
+  // 4-lane amax exchange needs the whole warp)
+  for (int it = 0; it < nit; ++it) {
+    const int v = (tid + it * kBThreads) * 8;
+    const bool ok = v < Dq;
+    float yv[8], w[8];
+    if (ok) {
+      load8(norm_w + d0 + v, w);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float h = 0.f;
+#pragma unroll
+        for (int c = 0; c < kHC; ++c) h = fmaf(p[c], xs[c * Dq + v + i], h);
+        yv[i] = h * rstd * w[i];
+      }
+      if (hb) store8_bf16(hb + (int64_t)t * D + d0 + v, yv);
+      if (hf) store8_f32(hf + (int64_t)t * D + d0 + v, yv);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) yv[i] = 0.f;
+    }
+    if (q) quant8(yv, q + (int64_t)t * D + d0 + v, sf, t, d0 + v, kb, ok);
   }
 }
 
@@ -797,6 +1000,44 @@ int b200_hc_pre(const float* raw, int ldr, int parts, int pstride, const float* 
                    iters, eps, inv_width, reinterpret_cast<const __nv_bfloat16*>(X), D, norm_w, norm_eps, post, comb,
                    q, sf, reinterpret_cast<__nv_bfloat16*>(hb), hf);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
+}
+
+int b200_hc_boundary(void* X, int T, int hc, int D, const void* y, int64_t ldy, const float* post_in,
+                     const float* comb_in, const float* fn, int M, const float* scale, const float* base, int mode,
+                     int iters, float eps, float inv_width, const float* norm_w, float norm_eps, float* post,
+                     float* comb, uint8_t* q, uint8_t* sf, void* hb, float* hf, cudaStream_t st) {
+  using namespace b200::v4;
+  if (T <= 0) return 0;
+  if (hc != kHC || M > kBMaxM || M < kHC || (mode == 0 && (!post || !comb || M < 2 * kHC + kHC * kHC))) return -1;
+  if (y && (!post_in || !comb_in)) return -1;
+  int C = 0;
+  for (int c = 8; c >= 1; c >>= 1)
+    if (D % (32 * c) == 0 && D / c >= 128) { C = c; break; }
+  if (C == 0 || D % 8 || (reinterpret_cast<uintptr_t>(fn) & 15)) return -2;
+  const int Dq = D / C;
+  const size_t smem = size_t(kHC) * Dq * sizeof(float);
+  if (smem > 200 * 1024) return -3;
+  auto kern = hc_boundary_kernel;
+  if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(C, T);
+  cfg.blockDim = dim3(kBThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = b200::pdl_enabled() ? 2 : 1;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kern, reinterpret_cast<__nv_bfloat16*>(X), D, C,
+                                             reinterpret_cast<const __nv_bfloat16*>(y), ldy, post_in, comb_in, fn, M,
+                                             scale, base, mode, iters, eps, inv_width, norm_w, norm_eps, post, comb, q,
+                                             sf, reinterpret_cast<__nv_bfloat16*>(hb), hf);
+  return err == cudaSuccess ? 0 : 1000 + int(err);
 }
 
 int b200_hc_mean(const void* X, int T, int hc, int D, void* out, cudaStream_t st) {

@@ -176,6 +176,28 @@ void compress_store(const at::Tensor& g, const at::Tensor& bias, const at::Tenso
       "compress_store");
 }
 
+void hc_boundary(const at::Tensor& X, c10::optional<at::Tensor> y, c10::optional<at::Tensor> post_in,
+                 c10::optional<at::Tensor> comb_in, const at::Tensor& fn, const at::Tensor& scale,
+                 const at::Tensor& base, int64_t mode, int64_t iters, double eps, const at::Tensor& norm_w,
+                 double norm_eps, c10::optional<at::Tensor> post, c10::optional<at::Tensor> comb,
+                 c10::optional<at::Tensor> q, c10::optional<at::Tensor> sf, c10::optional<at::Tensor> hb,
+                 c10::optional<at::Tensor> hf) {
+  TORCH_CHECK(X.is_cuda() && X.dim() == 3 && X.is_contiguous() && X.scalar_type() == at::kBFloat16, "X bf16 [T,hc,D]");
+  TORCH_CHECK(fn.is_contiguous() && fn.scalar_type() == at::kFloat && fn.size(1) == X.size(1) * X.size(2),
+              "fn fp32 [M, hc*D]");
+  const bool has_y = y.has_value() && y->defined();
+  if (has_y)
+    TORCH_CHECK(y->scalar_type() == at::kBFloat16 && y->stride(1) == 1 && y->size(0) == X.size(0), "y bf16 [T, D]");
+  const c10::cuda::CUDAGuard g(X.device());
+  const int T = X.size(0), hc = X.size(1), D = X.size(2);
+  chk(b200_hc_boundary(X.data_ptr(), T, hc, D, has_y ? y->data_ptr() : nullptr, has_y ? y->stride(0) : 0,
+                       optr<float>(post_in), optr<float>(comb_in), fn.data_ptr<float>(), fn.size(0),
+                       scale.data_ptr<float>(), base.data_ptr<float>(), mode, iters, float(eps), 1.f / float(hc * D),
+                       norm_w.data_ptr<float>(), float(norm_eps), optr<float>(post), optr<float>(comb),
+                       optr<uint8_t>(q), optr<uint8_t>(sf), optr<void>(hb), optr<float>(hf), cur()),
+      "hc_boundary");
+}
+
 void mqa_q_prep(const at::Tensor& q, const at::Tensor& pos, const at::Tensor& table, int64_t rd, at::Tensor q8,
                 at::Tensor qs) {
   TORCH_CHECK(q.is_cuda() && q.dim() == 3 && q.size(2) == 512 && q.stride(2) == 1 && q.scalar_type() == at::kBFloat16,
@@ -220,6 +242,7 @@ void register_v4(pybind11::module& m) {
   m.def("hc_post", &hc_post);
   m.def("l2_prefetch", &l2_prefetch);
   m.def("hc_pre", &hc_pre);
+  m.def("hc_boundary", &hc_boundary);
   m.def("hc_mean", &hc_mean);
   m.def("hc_embed", &hc_embed);
   m.def("engram_hash", &engram_hash);

@@ -311,3 +311,53 @@ def test_compressed_sparse_attention_kernels(r):
     exp = ops.mqa_attention(q.float(), cache, 0.7, fbc, cfg.softmax_scale, ps, snk, table.cpu(), rd, sel,
                             comp=(kv1, r))
     assert rel_err(o.cpu(), exp) < 3e-2, rel_err(o.cpu(), exp)
+
+
+@pytest.mark.parametrize("T,D,head,post", [(5, 1024, False, True), (64, 5120, False, True), (64, 5120, False, False),
+                                           (9, 1024, True, True), (200, 5120, True, False)])
+def test_hc_boundary_fused(T, D, head, post):
+    """The one-kernel boundary (hc_post + fp32 mixes + coefficients + normed
+    input, a cluster of CTAs per row) against the fp32 reference of hc_post
+    followed by hc_pre, and against the unfused GPU path."""
+    from b200ds.ops import HcWeights, cuda, ref
+    from b200ds.ops.quant import dequant_mxfp8
+    from b200ds.config import small_v4_gpu_config
+    cfg = small_v4_gpu_config()
+    X = _streams(T, D, 3)
+    M = 4 if head else 24
+    g = torch.Generator(device=DEV).manual_seed(4)
+    hw = HcWeights(torch.randn(M, 4 * D, device=DEV, generator=g) * 0.02,
+                   torch.rand(1 if head else 3, device=DEV) + 0.5, torch.randn(M, device=DEV, generator=g))
+    w = torch.rand(D, device=DEV) + 0.5
+    y = torch.randn(T, D, device=DEV).to(torch.bfloat16) if post else None
+    p_in = torch.rand(T, 4, device=DEV) * 2
+    c_in = torch.rand(T, 16, device=DEV)
+    carry = (y, p_in, c_in) if post else None
+    # fp32 reference
+    Xr = X.float()
+    if post:
+        Xr = ref.hc_post(Xr, y.float(), p_in, c_in.view(T, 4, 4)).to(torch.bfloat16).float()
+    ss = Xr.pow(2).sum((1, 2))
+    raw = Xr.flatten(1) @ hw.fn.T
+    if head:
+        pre = ref.hc_head_coeffs(raw, ss, hw.scale, hw.base, 4, 4 * D, cfg.hc_eps)
+    else:
+        pre, post_r, comb_r = ref.hc_coeffs(raw, ss, hw.scale, hw.base, 4, 4 * D, cfg.hc_sinkhorn_iters, cfg.hc_eps)
+    h_ref = ref.rmsnorm(ref.hc_combine(Xr, pre), w, 1e-6)
+
+    class _Q:
+        quantized = True
+    X1 = X.clone()
+    a, p2, c2 = cuda.hc_boundary(X1, carry, hw, w, 1e-6, cfg, _Q(), head, True)
+    assert torch.allclose(X1.float(), Xr, atol=1e-2, rtol=1e-2)
+    if not head:
+        assert torch.allclose(p2, post_r, atol=2e-4, rtol=1e-4)
+        assert torch.allclose(c2.view(T, 4, 4), comb_r, atol=2e-4, rtol=1e-3)
+    assert rel_err(a.hf, h_ref) < 5e-3
+    assert rel_err(dequant_mxfp8(a.q, a.sf), h_ref) < 4e-2
+    # same as the unfused GPU kernels (hc_post, stats GEMM, hc_pre)
+    X2 = X.clone()
+    ss2 = cuda.hc_post(X2, *carry) if post else X2.float().pow(2).sum((1, 2))
+    b, p3, c3 = cuda.hc_pre(X2, ss2, hw, w, 1e-6, cfg, _Q(), head, True)
+    assert torch.equal(X1, X2)
+    assert rel_err(a.hf, b.hf) < 2e-3
