@@ -493,8 +493,8 @@ __global__ void __launch_bounds__(kBThreads) hc_boundary_kernel(
 #pragma unroll
       for (int m = 0; m < kBMaxM; ++m) {
         if (m < M) {
-          const float4 a = __ldg(reinterpret_cast<const float4*>(f + m * K));
-          const float4 b = __ldg(reinterpret_cast<const float4*>(f + m * K + 4));
+          const float4 a = *reinterpret_cast<const float4*>(f + m * K);
+          const float4 b = *reinterpret_cast<const float4*>(f + m * K + 4);
           acc[m] = fmaf(xv[0], a.x, fmaf(xv[1], a.y, fmaf(xv[2], a.z, fmaf(xv[3], a.w, acc[m]))));
           acc[m] = fmaf(xv[4], b.x, fmaf(xv[5], b.y, fmaf(xv[6], b.z, fmaf(xv[7], b.w, acc[m]))));
         }
