@@ -164,7 +164,7 @@ def swiglu_splits(T: int, I: int, K: int) -> int:
         return 1
     tiles = I // 128
     ktiles = K // 128
-    for s in (4, 2):
+    for s in (8, 4, 2):
         if tiles * s <= 148 and ktiles // s >= 4:
             return s
     return 1

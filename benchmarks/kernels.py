@@ -317,6 +317,11 @@ def run_v4(T: int, iters: int, D: int = 5120, H: int = 64, ctx: int = 1040):
     t = timed(lambda: cuda.hc_pre(X, ss, hw, w, 1e-6, cfg, _Q(), False, False), iters)
     report("v4_hc_pre", f"T={T} hc=4 D={D} (stats GEMM + coeff/Sinkhorn/combine/norm/MXFP8)", t,
            nbytes=T * 4 * D * 2 * 2 + 128 * 4 * D * 2 + T * D, note="3 launches incl. the zeroed raw buffer")
+    # the same boundary as one kernel (post + fp32 mixes + coefficients + normed input)
+    t = timed(lambda: cuda.hc_boundary(X, (y, post, comb), hw, w, 1e-6, cfg, _Q(), False, False), iters)
+    report("v4_hc_boundary", f"T={T} hc=4 D={D} (hc_post + mixes + coeff/Sinkhorn/combine/norm/MXFP8, one kernel)",
+           t, nbytes=T * 4 * D * 2 * 2 + T * D * 2 + 24 * 4 * D * 4 + T * D,
+           note="fn read from L2 by every row's cluster; compare with v4_hc_post + v4_hc_pre")
     ps = 64
     pages = (ctx + ps - 1) // ps
     table = cos_sin_table(cfg, 4096, device=dev)

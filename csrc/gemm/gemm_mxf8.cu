@@ -136,7 +136,7 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
   if (nk < 0) nk = 0;
   // A cluster's CTAs must all reach its barriers: an empty split stays and
   // contributes zeros.
-  if (nk == 0 && EPI != kEpiClusterSplit) return;
+  if (nk == 0 && !C::kCluster) return;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
@@ -360,11 +360,14 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
     const uint32_t red_local = smem_u32(sA);
     const int tmax = rows - tile_t * BN;
     if constexpr (EPI == kEpiClusterSwiglu) {
-      const int blocks = rpc / 32;
-      for (int wi = warp; wi < BN * blocks; wi += kThreads / 32) {
-        const int col = wi / blocks;
+      // work item = (token column, 32-channel block), spread over the
+      // cluster's warps (any split count: a block may belong to any rank)
+      constexpr int kBlocks = kTileM / 32;
+      constexpr int kWarps = kThreads / 32;
+      for (int wi = int(rank) * kWarps + warp; wi < BN * kBlocks; wi += S * kWarps) {
+        const int col = wi / kBlocks;
         if (col >= tmax) continue;                     // uniform per warp
-        const int rr = rank * rpc + (wi % blocks) * 32 + lane;
+        const int rr = (wi % kBlocks) * 32 + lane;
         float g = 0.f, u = 0.f;
         for (int q = 0; q < S; ++q) {
           g += ld_dsmem_f32(mapa_shared(red_local + (uint32_t)(rr * kW + col) * 4u, q));
@@ -565,7 +568,7 @@ int b200_gemm_mxf8(const GemmArgs* a, cudaStream_t st) {
       if (g || a->splits < 2 || a->splits > 8 || (128 % a->splits) != 0 || a->t > 128 || !a->ar_peers) return -14;
       return launch_bn<kEpiClusterPush, false>(*a, st);
     case kEpiClusterSwiglu:
-      if (g || a->splits < 2 || a->splits > 4 || a->t > 128 || a->inter % 128) return -15;
+      if (g || a->splits < 2 || a->splits > 8 || a->t > 128 || a->inter % 128) return -15;
       return launch_bn<kEpiClusterSwiglu, false>(*a, st);
   }
   return -12;

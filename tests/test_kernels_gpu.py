@@ -98,7 +98,8 @@ def test_gemm_splitk_fp32():
     assert rel_err(out, exp) < 1e-4
 
 
-@pytest.mark.parametrize("T,splits", [(1, 1), (20, 1), (64, 1), (200, 1), (1, 4), (20, 2), (64, 4), (128, 2)])
+@pytest.mark.parametrize("T,splits", [(1, 1), (20, 1), (64, 1), (200, 1), (1, 4), (20, 2), (64, 4), (128, 2), (64, 8),
+                                      (5, 8)])
 def test_gemm_swiglu_quant(T, splits):
     from b200ds.ops import QAct, cuda, ref
     from b200ds.ops.quant import dequant_mxfp8
