@@ -356,10 +356,11 @@ def moe_tiles(rows_per_expert: float):
     """(FC1, FC2) token tiles of the grouped GEMMs.  Decode-sized experts
     take the smallest tile that holds their rows (weight streaming); from 128
     rows per expert FC1 runs 128-token tiles (gate + up into one TMEM
-    accumulator) and from 256 rows FC2 runs 256-token tiles, which halve the
-    shared-memory traffic per MMA of the compute-bound prefill GEMMs."""
+    accumulator).  FC2 stays at 128 tokens: N = 256 block-scaled MMAs need
+    the B scale factors of tokens 128-255 in a TMEM layout this kernel does
+    not stage (the 256-token tile produced wrong sums)."""
     bn1 = 128 if rows_per_expert >= 128 else moe_tile_n(rows_per_expert, 64)
-    bn2 = 256 if rows_per_expert >= 256 else moe_tile_n(rows_per_expert, 128)
+    bn2 = moe_tile_n(rows_per_expert, 128)
     return (tactics.pick("moe_tile_fc1", bn1, rows_per_expert=rows_per_expert),
             tactics.pick("moe_tile_fc2", bn2, rows_per_expert=rows_per_expert))
 

@@ -31,7 +31,7 @@ _LEGAL = {
         and ctx.get("N", 0) // 128 * v <= ctx.get("max_ctas", 1 << 30))),
     "moe_tile": lambda v, ctx: v in (16, 32, 64, 128) and v <= ctx.get("cap", 128),
     "moe_tile_fc1": lambda v, ctx: v in (16, 32, 64, 128),
-    "moe_tile_fc2": lambda v, ctx: v in (16, 32, 64, 128, 256),
+    "moe_tile_fc2": lambda v, ctx: v in (16, 32, 64, 128),
     "mla_splits": lambda v, ctx: isinstance(v, int) and 1 <= v <= 16,
 }
 

@@ -485,9 +485,6 @@ static int launch_bn(const GroupedArgs& a, cudaStream_t st) {
     case 32: return launch<32, EPI, FP4>(a, st);
     case 64: return launch<64, EPI, FP4>(a, st);
     case 128: return launch<128, EPI, FP4>(a, st);
-    case 256:
-      if constexpr (EPI != kEpiSwiglu) return launch<256, EPI, FP4>(a, st);
-      return -4;
   }
   return -4;
 }

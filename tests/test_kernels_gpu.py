@@ -749,13 +749,14 @@ def test_l2_prefetch_runs_and_captures():
 
 @pytest.mark.parametrize("fp4", [False, True])
 def test_moe_experts_prefill_tiles(fp4):
-    """Prefill-sized experts (>= 256 rows each): FC1 on 128-token tiles and
-    FC2 on 256-token tiles with one TMEM accumulator, against the CPU path."""
+    """Prefill-sized experts (>= 128 rows each): FC1 (gate + up) on
+    128-token tiles with one TMEM accumulator, FC2 on 128-token tiles,
+    against the CPU path."""
     from b200ds.ops import ExpertWeights, QAct, cuda
     from b200ds.ops.quant import MXFP8Tensor, NVFP4Tensor, dequant_mxfp8
     import b200ds.ops as ops
     T, H, I, E, K = 512, 1024, 256, 8, 4            # 256 rows per expert
-    assert cuda.moe_tiles(T * K / E) == (128, 256)
+    assert cuda.moe_tiles(T * K / E) == (128, 128)
     torch.manual_seed(7)
     ids = torch.stack([torch.randperm(E, device=DEV)[:K] for _ in range(T)]).int()
     wts = torch.rand(T, K, device=DEV)
