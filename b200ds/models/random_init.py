@@ -159,7 +159,8 @@ def build_random_model(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState, 
         # Random bytes need no re-layout: with 64 or fewer experts per GPU
         # the grouped GEMM reads them as contiguous 128 x 128-byte tiles
         # (measured: FC1 at 32 experts/GPU 0.78 -> 0.83 of copy bandwidth).
-        expert_sets.append(ExpertWeights(first=first, count=per, w13=w13, w2=w2, inter=I, tiled=per <= 64))
+        expert_sets.append(ExpertWeights(first=first, count=per, w13=w13, w2=w2, inter=I, tiled=per <= 64,
+                                         random_init=True))
     moe_idx = 0
     for i in range(cfg.num_hidden_layers):
         if cfg.is_moe_layer(i):
@@ -224,7 +225,8 @@ def build_random_model_v4(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelStat
             w13, w2 = rand_nvfp4(per, 2 * I, h, dev, sd), rand_nvfp4(per, h, I, dev, sd)
         else:
             w13, w2 = rand_mx((per,), 2 * I, h, dev, sd), rand_mx((per,), h, I, dev, sd)
-        expert_sets.append(ExpertWeights(first=first, count=per, w13=w13, w2=w2, inter=I, tiled=per <= 64))
+        expert_sets.append(ExpertWeights(first=first, count=per, w13=w13, w2=w2, inter=I, tiled=per <= 64,
+                                         random_init=True))
     layers = []
     moe_idx = 0
     for i in range(cfg.num_hidden_layers):

@@ -73,6 +73,8 @@ class ExpertWeights:
     # weights stored as contiguous 128-row x 128-byte tiles (GPU serving
     # layout, see ops.quant.tile_rows128)
     tiled: bool = False
+    # random-init bytes (benchmarks): any layout reads as the same distribution
+    random_init: bool = False
 
 
 @dataclass
@@ -297,6 +299,8 @@ def mla_attention(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size, to
         from . import baseline
         if fb.is_decode and page_size in (32, 64) and baseline.flashinfer_ok():
             return baseline.mla_decode_flashinfer(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size)
+        if fb.is_decode and int(q_abs.shape[0]) == int(fb.block_table.shape[0]):
+            return baseline.mla_decode_torch(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size)
         return baseline.mla_prefill_torch(q_abs, q_pe, cache, kv_scale, fb, softmax_scale, page_size)
     out = ref.mla_attention(q_abs, q_pe, cache, kv_scale, fb.block_table, fb.seq_lens, fb.q_seq,
                             fb.positions, softmax_scale, page_size, topk)
@@ -380,10 +384,12 @@ def moe_experts(h, w: torch.Tensor, ids: torch.Tensor, ex: ExpertWeights, out_dt
         if _IMPL == "native":
             return _native().moe_experts(h, w, ids, ex, out_dtype, n_experts_total, combine)
         from . import baseline
+        xb = h.hf if isinstance(h, QAct) and h.hf is not None else (
+            dequant_mxfp8(h.q, h.sf).to(torch.bfloat16) if isinstance(h, QAct) else h.to(torch.bfloat16))
         if baseline.flashinfer_ok() and n_experts_total is not None:
-            xb = h.hf if isinstance(h, QAct) and h.hf is not None else (
-                dequant_mxfp8(h.q, h.sf).to(torch.bfloat16) if isinstance(h, QAct) else h.to(torch.bfloat16))
             return baseline.moe_experts_flashinfer(xb.contiguous(), w, ids, ex, n_experts_total).to(out_dtype)
+        if baseline.grouped_mx_ok(xb.device):
+            return baseline.moe_experts_grouped(xb, w, ids, ex, out_dtype)
         return baseline.moe_experts(h if isinstance(h, QAct) else quant(h), w, ids, ex, out_dtype)
     xf = to_float(h)
     T = xf.shape[0]

@@ -91,12 +91,144 @@ _FI_WS = {}
 
 
 def flashinfer_ok() -> bool:
+    """FlashInfer's trtllm-gen launchers are JIT-compiled on first use (many
+    minutes offline); the arm uses them only when B200_BASELINE_FLASHINFER=1
+    and the modules import."""
+    import os
+    if os.environ.get("B200_BASELINE_FLASHINFER", "0") != "1":
+        return False
     try:
         import flashinfer.fused_moe  # noqa: F401
         import flashinfer.decode  # noqa: F401
         return True
     except Exception:
         return False
+
+
+# ---------------------------------------------------------------------------
+# Library MoE and decode attention (no FlashInfer): PyTorch ops with static
+# shapes (no host synchronisation, CUDA-graph capturable) around the MXFP8
+# grouped GEMM of the PyTorch build (F.scaled_grouped_mm: e4m3 operands with
+# UE8M0 per-32 scales in the 32_4_4 swizzled layout, which is the layout our
+# MXFP8 tensors already use).
+# ---------------------------------------------------------------------------
+_GROUPED_MX_OK = None
+
+
+def _scaled_grouped(aq, asf, w, offs):
+    """[R, K] MXFP8 rows (groups at offs, 128-row aligned) x expert weights
+    w [E, N, K] (MXFP8) -> [R, N] bf16."""
+    import torch.nn.functional as F
+    R, K = aq.shape
+    E, N = w.data.shape[0], w.data.shape[1]
+    sw = F.SwizzleType.SWIZZLE_32_4_4
+    return F.scaled_grouped_mm(aq.view(torch.float8_e4m3fn), w.data.view(torch.float8_e4m3fn).transpose(-2, -1),
+                               asf.view(torch.float8_e8m0fnu).view(R, K // 32), F.ScalingType.BlockWise1x32,
+                               w.sf.view(torch.float8_e8m0fnu).view(E, N, K // 32), F.ScalingType.BlockWise1x32,
+                               swizzle_a=sw, swizzle_b=sw, offs=offs, output_dtype=torch.bfloat16)
+
+
+def moe_experts_grouped(x: torch.Tensor, w: torch.Tensor, ids: torch.Tensor, ex, out_dtype=torch.bfloat16):
+    """Routed experts of this rank through two library grouped MXFP8 GEMMs:
+    the (token, choice) pairs of local experts are sorted by expert into
+    128-row-aligned groups (PyTorch scatter / sort / cumsum on the device),
+    quantized per 32, FC1 -> SwiGLU -> requantize -> FC2, and the weighted
+    rows are summed per token.  Experts in the tiled serving layout are
+    untiled once (random-init bytes are read row-major as they are: the
+    native kernels' tiled reading of the same bytes is another random matrix
+    of the same distribution)."""
+    if getattr(ex, "tiled", False) and not getattr(ex, "random_init", False):
+        ex = _untiled(ex)
+    T, H = x.shape
+    K = ids.shape[1]
+    E = ex.count
+    dev = x.device
+    e = ids.reshape(-1).long() - ex.first
+    valid = (e >= 0) & (e < E)
+    ek = torch.where(valid, e, torch.full_like(e, E))
+    counts = torch.zeros(E + 1, dtype=torch.long, device=dev).scatter_add_(0, ek, torch.ones_like(ek))[:E]
+    padded = (counts + 127) // 128 * 128
+    pstart = torch.cumsum(padded, 0) - padded
+    ustart = torch.cumsum(counts, 0) - counts
+    order = torch.argsort(ek, stable=True)
+    es = ek.index_select(0, order)
+    ec = es.clamp(max=E - 1)
+    rank = torch.arange(order.numel(), device=dev) - ustart.index_select(0, ec)
+    R = (T * K + 127) // 128 * 128 + E * 128 + 128          # static bound; the last row takes unrouted pairs
+    dest = torch.where(es < E, pstart.index_select(0, ec) + rank, torch.full_like(rank, R - 1))
+    tok = order // K
+    rows = torch.zeros(R, H, dtype=torch.bfloat16, device=dev)
+    rows.index_copy_(0, dest, x.to(torch.bfloat16).index_select(0, tok))
+    rows[R - 1].zero_()
+    offs = torch.cumsum(padded, 0).to(torch.int32)
+    aq, asf = quant_mxfp8_ref(rows)
+    y1 = _scaled_grouped(aq, asf, ex.w13, offs)
+    I = ex.inter
+    h = torch.nn.functional.silu(y1[:, :I].float()) * y1[:, I:2 * I].float()
+    hq, hsf = quant_mxfp8_ref(h)
+    y2 = _scaled_grouped(hq, hsf, ex.w2, offs)
+    wp = (w.reshape(-1).float().index_select(0, order) * (es < E)).unsqueeze(1)
+    contrib = y2.index_select(0, dest).float() * wp
+    out = torch.zeros(T, H, dtype=torch.float32, device=dev).index_add_(0, tok, contrib)
+    return out.to(out_dtype)
+
+
+_UNTILED = {}
+
+
+def _untiled(ex):
+    from .quant import untile_rows128
+    import dataclasses
+    key = id(ex)
+    if key not in _UNTILED:
+        u = lambda t: MXFP8Tensor(untile_rows128(t.data.view(torch.uint8)).view(t.data.dtype), t.sf, t.rows)
+        _UNTILED[key] = dataclasses.replace(ex, w13=u(ex.w13), w2=u(ex.w2), tiled=False)
+    return _UNTILED[key]
+
+
+def grouped_mx_ok(dev) -> bool:
+    """Whether this PyTorch build runs the MXFP8 grouped GEMM here (checked
+    once on a tiny case against the per-expert library GEMM)."""
+    global _GROUPED_MX_OK
+    if _GROUPED_MX_OK is None:
+        try:
+            import torch.nn.functional as F  # noqa: F401
+            from . import ExpertWeights
+            g = torch.Generator(device=dev).manual_seed(0)
+            E, H, I, T, K = 2, 256, 128, 8, 2
+            mk = lambda n, k: MXFP8Tensor(*quant_mxfp8_ref(torch.randn(E * n, k, device=dev, generator=g) * 0.1))
+            w13, w2 = mk(2 * I, H), mk(H, I)
+            ex = ExpertWeights(0, E, MXFP8Tensor(w13.data.view(E, 2 * I, H), w13.sf.view(E, -1)),
+                               MXFP8Tensor(w2.data.view(E, H, I), w2.sf.view(E, -1)), I)
+            x = torch.randn(T, H, device=dev, generator=g)
+            ids = torch.stack([torch.randperm(E, device=dev)[:K] for _ in range(T)]).int()
+            wt = torch.rand(T, K, device=dev)
+            got = moe_experts_grouped(x, wt, ids, ex, torch.float32)
+            want = moe_experts(quant(x), wt, ids, ex, torch.float32)
+            _GROUPED_MX_OK = bool(((got - want).norm() / want.norm()).item() < 0.1)
+        except Exception:
+            _GROUPED_MX_OK = False
+    return _GROUPED_MX_OK
+
+
+def mla_decode_torch(q_abs: torch.Tensor, q_pe: torch.Tensor, cache: torch.Tensor, kv_scale: float, fb,
+                     softmax_scale: float, page_size: int) -> torch.Tensor:
+    """Absorbed MLA decode (one query row per sequence) in PyTorch ops with
+    static shapes: every sequence's block-table rows are gathered and
+    dequantized to bf16 [B, pages * page_size, 576], S = q . K^T by cuBLAS
+    batched GEMM, positions past the query masked, fp32 softmax, O = P . V.
+    Returns the latent output [B, H, 512] bf16."""
+    B, H, L = q_abs.shape
+    bt = fb.block_table.long()
+    S = bt.shape[1] * page_size
+    slots = (bt.unsqueeze(-1) * page_size + torch.arange(page_size, device=bt.device)).view(B, S)
+    kv = (cache.index_select(0, slots.view(-1)).float() * kv_scale).to(torch.bfloat16).view(B, S, -1)
+    q = torch.cat([q_abs.to(torch.bfloat16), q_pe.to(torch.bfloat16)], -1)
+    s = torch.matmul(q, kv.transpose(1, 2)).float() * softmax_scale                 # [B, H, S]
+    mask = torch.arange(S, device=q.device).unsqueeze(0) > fb.positions.long().unsqueeze(1)
+    s.masked_fill_(mask.unsqueeze(1), float("-inf"))
+    p = torch.softmax(s, -1).to(torch.bfloat16)
+    return torch.matmul(p, kv[..., :L])
 
 
 def _block128_scales(t: MXFP8Tensor, E: int, N: int, K: int) -> torch.Tensor:
