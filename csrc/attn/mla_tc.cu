@@ -374,9 +374,12 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
     // eight warps never disagree on the barrier count.
     bool ok = true;
     for (int i = 0; i < nt; ++i) {
+      const int tok0 = k_lo + i * kTile;
+      // the row's list entry is loaded before the wait for S (it does not depend on it)
+      int pos = 0;
+      if (SPARSE && tok0 + row < k_hi) pos = __ldcg(p.topk + (int64_t)t * p.topk_n + tok0 + row);
       if (ok && !mbar_wait(&s_full[i & 1], (i >> 1) & 1, p.err)) ok = false;
       tc_fence_after();
-      const int tok0 = k_lo + i * kTile;
       float x[NC];
       {
         const uint32_t base = tmem + S::kTmemS + (i & 1) * HB + hc0 + (uint32_t(sub * 32) << 16);
@@ -393,10 +396,7 @@ mla_tc_kernel(const __grid_constant__ CUtensorMap tm_q_lat, const __grid_constan
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[i & 1]);      // this warp's S^T columns are read
       bool valid = tok0 + row < k_hi;
-      if (SPARSE && valid) {
-        const int pos = __ldcg(p.topk + (int64_t)t * p.topk_n + tok0 + row);
-        valid = (pos >= 0 && pos < n) || (p.ratio2 > 0 && pos >= kMlaCompFlag);
-      }
+      if (SPARSE && valid) valid = (pos >= 0 && pos < n) || (p.ratio2 > 0 && pos >= kMlaCompFlag);
       float v[NC];
 #pragma unroll
       for (int j = 0; j < NC; ++j) {
