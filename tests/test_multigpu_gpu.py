@@ -187,15 +187,16 @@ def _v4_rank(rank, world):
     import torch.distributed as dist
     from b200ds import ops
     from b200ds.config import EngineConfig, small_v4_gpu_config
+    from b200ds import build_model_from
     from b200ds.models.batch import build_batch
-    from b200ds.models.loader import build_model
     from b200ds.models.reference_v4 import init_weights_v4
     from b200ds.parallel.state import init_parallel
     ps = init_parallel(backend="nccl", timeout_s=60)
     ops.set_impl("native")
     cfg = small_v4_gpu_config()
     sd = init_weights_v4(cfg, 0)
-    m = build_model(cfg, EngineConfig(tp_size=world, ep_size=world, comm_impl="fused"), ps, sd, device=ps.device)
+    m = build_model_from(cfg, EngineConfig(tp_size=world, ep_size=world, comm_impl="fused"), sd, device=ps.device,
+                         ps=ps)
     m.allocate_kv(8)
     g = torch.Generator().manual_seed(5)
     toks = torch.randint(0, cfg.vocab_size, (40,), generator=g).tolist()
