@@ -83,11 +83,28 @@ class FusedAllReduce:
         from ..ops.cuda import alloc_qact
         T, H = a.shape
         x = a if (a.dtype == torch.bfloat16 and a.is_contiguous()) else a.to(torch.bfloat16).contiguous()
-        bases, epoch, ticket, mc = self._push_target()
-        _C.ar_push(x, bases, self.rank, self.max_tokens, epoch, ticket, self.push_ctas, mc=mc)
         y = torch.empty(T, H, dtype=torch.bfloat16, device=a.device) if (keep_bf16 or not quantize) else None
         qa = alloc_qact(T, H, a.device) if quantize else None
+        if self._one_kernel():
+            _C.ar_fused_norm(x, None, None, T, self.bases, self.rank, self.max_tokens, self.epoch, self.ticket,
+                             residual, w, eps, y, qa.q if qa else None, qa.sf if qa else None, self.err)
+            return self._done(y, qa, residual)
+        bases, epoch, ticket, mc = self._push_target()
+        _C.ar_push(x, bases, self.rank, self.max_tokens, epoch, ticket, self.push_ctas, mc=mc)
         return self._reduce(T, H, 1, residual, w, eps, y, qa)
+
+    def _one_kernel(self) -> bool:
+        """Push, per-CTA arrivals and reduce + norm in one launch (push mode;
+        the NVLS path keeps its two kernels)."""
+        from ..utils import levers
+        return self.nvls is None and levers.on("ar_one_kernel")
+
+    @staticmethod
+    def _done(y, qa, residual):
+        if qa is not None:
+            qa.hf = y
+            return qa, residual
+        return y, residual
 
     def _outs(self, T, H, dev, quantize, keep_bf16=True):
         from ..ops.cuda import alloc_qact
@@ -135,6 +152,11 @@ class FusedAllReduce:
         T = part.pair_row.shape[0]
         H = part.y.shape[1]
         add = part.add.to(torch.bfloat16).contiguous() if part.add is not None else None
+        if self._one_kernel():
+            y, qa = self._outs(T, H, part.y.device, quantize)
+            _C.ar_fused_norm(part.y, part.pair_row, add, T, self.bases, self.rank, self.max_tokens, self.epoch,
+                             self.ticket, residual, ln_w, eps, y, qa.q if qa else None, qa.sf if qa else None, self.err)
+            return self._done(y, qa, residual)
         bases, epoch, ticket, mc = self._push_target()
         _C.moe_combine_push(part.y, part.pair_row, add, bases, self.rank, self.max_tokens, epoch, ticket,
                             self.push_ctas, mc=mc)

@@ -129,6 +129,9 @@ register("l2_prefetch", "B200_L2_PREFETCH", True,
 register("ep_combine_epilogue", "B200_EP_COMBINE_EPILOGUE", True,
          "expert parallelism: the experts' FC2 epilogue stores each weighted pair row straight into its token's "
          "owner rank (no separate combine kernel, no local round trip of the FC2 rows)")
+register("ar_one_kernel", "B200_AR_ONE_KERNEL", True,
+         "push-mode all-reduces (and the TP MoE combine) run push + per-CTA arrivals + reduce + norm as one kernel "
+         "instead of a push kernel and a reduce kernel")
 register("hc_boundary", "B200_HC_BOUNDARY", False,
          "V4 family, decode-sized batches: hc_post + the mHC mixes (fp32, CUDA cores) + coefficients + the next "
          "sublayer's normed input as one kernel, a thread-block cluster per row")

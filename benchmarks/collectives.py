@@ -10,8 +10,11 @@ CUDA events on the launching stream, max over ranks.  Per token count M
 
 o_proj GEMM + all-reduce (bf16 partial [M, 7168], K = 16384 / N):
   * nccl_ar        NCCL all-reduce of the partial alone;
+  * nccl_ar_norm   NCCL all-reduce + residual add + RMSNorm in PyTorch ops
+                   (the library chain the fused kernels replace);
   * push_ar        our one-shot NVLink push + reduce (+residual +RMSNorm
-                   +MXFP8), the push protocol;
+                   +MXFP8) as one kernel (per-CTA arrivals);
+  * push2_ar       the same as a push kernel + a reduce kernel;
   * nvls_ar        the same through NVLink multicast (multimem.ld_reduce /
                    multimem.st in the switch), when the GPUs support it;
   * gemm_nccl      our MXFP8 GEMM + NCCL all-reduce;
@@ -124,7 +127,19 @@ def ar_part(ps, Ms):
         resid = torch.zeros(M, H, device=dev)
         res = {"part": "gemm_ar", "M": M, "n_gpus": W, "N": H, "K": K}
         res["nccl_ar_us"] = timed(lambda: dist.all_reduce(part), iters)
+
+        def nccl_norm():
+            # the library chain the fused kernels replace: NCCL all-reduce,
+            # residual add and RMSNorm in PyTorch ops
+            r = part.clone()
+            dist.all_reduce(r)
+            resid.add_(r.float())
+            return (resid * torch.rsqrt(resid.pow(2).mean(-1, keepdim=True) + 1e-6) * ln).to(torch.bfloat16)
+        res["nccl_ar_norm_us"] = timed(nccl_norm, iters)
         res["push_ar_us"] = timed(lambda: far_push.allreduce_add_rmsnorm(part, resid, ln, 1e-6, True), iters)
+        levers.set_switch("ar_one_kernel", False)
+        res["push2_ar_us"] = timed(lambda: far_push.allreduce_add_rmsnorm(part, resid, ln, 1e-6, True), iters)
+        levers.set_switch("ar_one_kernel", True)
         if far_nvls is not None:
             res["nvls_ar_us"] = timed(lambda: far_nvls.allreduce_add_rmsnorm(part, resid, ln, 1e-6, True), iters)
         res["gemm_nccl_us"] = timed(lambda: dist.all_reduce(oc.gemm(x, w)), iters)

@@ -29,6 +29,7 @@
 // bounded and reports an error code instead of hanging.
 #include "../common/ptx.cuh"
 #include "comm_dev.cuh"
+#include <algorithm>
 
 namespace b200 {
 namespace comm {
@@ -251,6 +252,113 @@ int b200_ar_reduce_norm(int T, int hidden, const ArPeers* peers, uint32_t* epoch
 // rank.  grid: `nctas` CTAs over the tokens.
 namespace b200 {
 namespace comm {
+// One-kernel push all-reduce (+ MoE combine) + residual + RMSNorm (+ MXFP8)
+// for decode-sized steps.  CTA c of G owns rows c, c + G, ... (the same grid
+// on every rank): it stores its rows' partial - x, or for the MoE the sum of
+// the token's local expert rows y[pair_row] plus the shared-expert row - into
+// recv[p][rank] of every rank, raises cta_cnt[p][c] on every rank
+// (red.release.sys after a system fence), waits (bounded) until all ranks
+// raised its own cta_cnt[p][c], then sums the world partials of its rows in
+// rank order and runs the row epilogue.  Rows meet only their own CTAs, so
+// no grid-wide publish sits between the stores and the reduction, and one
+// launch replaces the push + reduce pair.  The last CTA (ticket) zeroes this
+// parity's CTA counters and advances the epoch (parity reuse is two
+// all-reduces away, as for the two-kernel protocol).
+template <bool COMBINE>
+__global__ void __launch_bounds__(kThreads) ar_fused_norm_kernel(
+    const __nv_bfloat16* __restrict__ x, const int* __restrict__ pair_row, int K, const __nv_bfloat16* __restrict__ add,
+    int T, int hidden, ArPeers peers, uint32_t* epoch, uint32_t* ticket, float* residual, const float* __restrict__ w,
+    float eps, __nv_bfloat16* y, uint8_t* q, uint8_t* sf, uint32_t* err) {
+  __shared__ float red[32];
+  __shared__ int ok_s;
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  const int p = (*epoch) & 1;
+  const int G = gridDim.x, c = blockIdx.x;
+  uint8_t* mine = peers.base[peers.rank];
+  const int units = hidden >> 3;
+  for (int t = c; t < T; t += G) {
+    for (int u = threadIdx.x; u < units; u += kThreads) {
+      uint4 outv;
+      if constexpr (COMBINE) {
+        float acc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+        for (int j = 0; j < K; ++j) {
+          const int r = __ldcg(pair_row + t * K + j);
+          if (r < 0) continue;
+          const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(x + (int64_t)r * hidden) + u);
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h[i]);
+            acc[2 * i] += f.x;
+            acc[2 * i + 1] += f.y;
+          }
+        }
+        if (add) {
+          const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(add + (int64_t)t * hidden) + u);
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h[i]);
+            acc[2 * i] += f.x;
+            acc[2 * i + 1] += f.y;
+          }
+        }
+        __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&outv);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+      } else {
+        outv = __ldcg(reinterpret_cast<const uint4*>(x + (int64_t)t * hidden) + u);
+      }
+      for (int d = 0; d < peers.world; ++d) {
+        __nv_bfloat16* dst = recv_slot(peers.base[d], p, peers.rank, peers.world, peers.max_t, hidden);
+        *reinterpret_cast<uint4*>(dst + (int64_t)t * hidden + u * 8) = outv;
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int d = 0; d < peers.world; ++d)
+      asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(cta_counters(peers.base[d], p) + c), "r"(1u)
+                   : "memory");
+    int ok = 1;
+    const uint32_t* cnt = cta_counters(mine, p) + c;
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_sys(cnt) < (uint32_t)peers.world) {
+      if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+        atomicExch(err, kErrPeerTimeout);
+        ok = 0;
+        break;
+      }
+    }
+    ok_s = ok;
+  }
+  __syncthreads();
+  if (ok_s) {
+    for (int t = c; t < T; t += G) {
+      row_add_norm_quant(t, hidden, recv_slot(mine, p, 0, peers.world, peers.max_t, hidden),
+                         (int64_t)peers.max_t * hidden, peers.world, hidden, nullptr, nullptr, residual, w, eps, y, q,
+                         sf, red);
+      __syncthreads();
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t tk = atomicAdd(ticket, 1u);
+    if (tk == (uint32_t)G - 1) {
+      uint32_t* cnt = cta_counters(mine, p);
+      for (int i = 0; i < G; ++i) atomicExch(cnt + i, 0u);
+      *ticket = 0u;
+      __threadfence();
+      atomicAdd(epoch, 1u);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kThreads) moe_combine_push_kernel(const __nv_bfloat16* __restrict__ y,
                                                                      const int* __restrict__ pair_row, int T, int K,
                                                                      int hidden, const __nv_bfloat16* __restrict__ add,
@@ -498,5 +606,26 @@ int b200_ep_comb_reduce_norm(int T_r, int hidden, int K, const int* ids, const v
   b200::launch_pdl(b200::comm::ep_comb_reduce_norm_kernel, dim3(T_r), dim3(b200::comm::kThreads), 0, st, T_r, hidden,
                    K, ids, reinterpret_cast<const __nv_bfloat16*>(add), *peers, epoch, ticket, residual, w, eps,
                    reinterpret_cast<__nv_bfloat16*>(y), q, sf, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : 1;
+}
+
+int b200_ar_fused_norm(const void* x, const int* pair_row, int K, const void* add, int T, int hidden,
+                       const ArPeers* peers, uint32_t* epoch, uint32_t* ticket, float* residual, const float* w,
+                       float eps, void* y, uint8_t* q, uint8_t* sf, uint32_t* err, cudaStream_t st) {
+  if (T <= 0) return 0;
+  if (T > peers->max_t || hidden % 32 || hidden > b200::comm::kThreads * 8 * b200::comm::kMaxIt || peers->mc ||
+      (pair_row && K <= 0))
+    return -1;
+  const int G = std::min(T, std::min(148, kArMaxCtas));
+  const auto* xb = reinterpret_cast<const __nv_bfloat16*>(x);
+  const auto* ab = reinterpret_cast<const __nv_bfloat16*>(add);
+  auto* yb = reinterpret_cast<__nv_bfloat16*>(y);
+  if (pair_row)
+    b200::launch_pdl(b200::comm::ar_fused_norm_kernel<true>, dim3(G), dim3(b200::comm::kThreads), 0, st, xb, pair_row,
+                     K, ab, T, hidden, *peers, epoch, ticket, residual, w, eps, yb, q, sf, err);
+  else
+    b200::launch_pdl(b200::comm::ar_fused_norm_kernel<false>, dim3(G), dim3(b200::comm::kThreads), 0, st, xb,
+                     (const int*)nullptr, 0, (const __nv_bfloat16*)nullptr, T, hidden, *peers, epoch, ticket, residual,
+                     w, eps, yb, q, sf, err);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }

@@ -4,7 +4,13 @@
 #include <cuda_runtime.h>
 
 constexpr int kArMaxRanks = 8;
-constexpr int64_t kArRecvOff = 256;        // bytes: counters first, then the receive slots
+// Push all-reduce buffer: [0, 64) uint32 cnt[2][kArMaxRanks] (per-source
+// arrivals), [128, 192) NVLS cnt2, [kArCtaCntOff, +2 KB) uint32
+// cta_cnt[2][kArMaxCtas] (per-CTA arrivals of the one-kernel all-reduce),
+// then the receive slots from kArRecvOff.
+constexpr int kArMaxCtas = 256;
+constexpr int64_t kArCtaCntOff = 256;
+constexpr int64_t kArRecvOff = 4096;
 
 // Symmetric-buffer base pointers of every rank (UVA peer mappings).
 struct ArPeers {
@@ -50,6 +56,12 @@ int b200_ar_push(const void* x, int T, int hidden, const ArPeers* peers, const u
 int b200_ar_reduce_norm(int T, int hidden, const ArPeers* peers, uint32_t* epoch, uint32_t* ticket, int push_ctas,
                         float* residual, const float* w, float eps, void* y, uint8_t* q, uint8_t* sf, uint32_t* err,
                         cudaStream_t st);
+// One kernel: push (plain partial x, or with pair_row the MoE combine of the
+// local expert rows y + add) + per-CTA arrivals + reduce + residual +
+// RMSNorm (+ MXFP8) of the rows each CTA owns.  Push mode only (no NVLS).
+int b200_ar_fused_norm(const void* x, const int* pair_row, int K, const void* add, int T, int hidden,
+                       const ArPeers* peers, uint32_t* epoch, uint32_t* ticket, float* residual, const float* w,
+                       float eps, void* y, uint8_t* q, uint8_t* sf, uint32_t* err, cudaStream_t st);
 int b200_moe_combine_push(const void* y, const int* pair_row, int T, int K, int hidden, const void* add,
                           const ArPeers* peers, const uint32_t* epoch, uint32_t* ticket, int nctas, cudaStream_t st);
 // NVLS all-reduce + residual + RMSNorm (+ MXFP8): waits for every rank's

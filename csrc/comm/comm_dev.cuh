@@ -37,6 +37,10 @@ __device__ __forceinline__ __nv_bfloat16* push_slot(const ArPeers& p, int d, int
               : recv_slot(p.base[d], parity, p.rank, p.world, p.max_t, hidden);
 }
 
+__device__ __forceinline__ uint32_t* cta_counters(uint8_t* base, int parity) {
+  return reinterpret_cast<uint32_t*>(base + kArCtaCntOff) + parity * kArMaxCtas;
+}
+
 __device__ __forceinline__ uint32_t* counters2(uint8_t* base, int parity) {
   return reinterpret_cast<uint32_t*>(base + kNvlsCnt2Off) + parity * kArMaxRanks;
 }
