@@ -74,11 +74,15 @@ void ar_fused_norm(const at::Tensor& x, c10::optional<at::Tensor> pair_row, c10:
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() == 2, "x bf16 rows");
   TORCH_CHECK(residual.scalar_type() == at::kFloat && residual.is_contiguous(), "residual fp32");
   const bool comb = pair_row.has_value() && pair_row->defined();
-  if (comb) TORCH_CHECK(pair_row->scalar_type() == at::kInt && pair_row->is_contiguous() && pair_row->size(0) == T,
-                        "pair_row int32 [T, K]");
-  else TORCH_CHECK(x.size(0) >= T, "x holds T rows");
-  if (add.has_value() && add->defined())
+  if (comb) {
+    TORCH_CHECK(pair_row->scalar_type() == at::kInt && pair_row->is_contiguous() && pair_row->size(0) == T,
+                "pair_row int32 [T, K]");
+  } else {
+    TORCH_CHECK(x.size(0) >= T, "x holds T rows");
+  }
+  if (add.has_value() && add->defined()) {
     TORCH_CHECK(add->scalar_type() == at::kBFloat16 && add->is_contiguous(), "add bf16 [T, H]");
+  }
   const c10::cuda::CUDAGuard g(x.device());
   ArPeers p = make_peers(bases, rank, max_t);
   const int rc = b200_ar_fused_norm(x.data_ptr(), comb ? reinterpret_cast<const int*>(pair_row->data_ptr()) : nullptr,
