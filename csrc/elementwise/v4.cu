@@ -302,11 +302,11 @@ template <class Mix>
 __device__ __forceinline__ void hc_coeffs_warp(Mix mix, float rs, const float* scale, const float* base, int mode,
                                                int iters, float eps, float* pre_s, float* post_row,
                                                float* comb_row) {
-  const int l = threadIdx.x & 15;
+  const int ln = threadIdx.x & 31, l = threadIdx.x & 15;
   if (l < kHC) {
     const float pre = sigmoidf(scale[0] * rs * mix(l) + base[l]) + eps;
-    if (threadIdx.x < kHC) pre_s[l] = pre;
-    if (mode == 0 && threadIdx.x < kHC && post_row)
+    if (ln < kHC) pre_s[l] = pre;
+    if (mode == 0 && ln < kHC && post_row)
       post_row[l] = 2.f * sigmoidf(scale[1] * rs * mix(kHC + l) + base[kHC + l]);
   }
   if (mode == 0) {
@@ -329,7 +329,7 @@ __device__ __forceinline__ void hc_coeffs_warp(Mix mix, float rs, const float* s
       csum += __shfl_xor_sync(0xffffffffu, csum, 8);
       m = m / (csum + eps);
     }
-    if (threadIdx.x < 16 && comb_row) comb_row[l] = m;
+    if (ln < 16 && comb_row) comb_row[l] = m;
   }
 }
 
@@ -400,193 +400,250 @@ __global__ void __launch_bounds__(kThreads) hc_pre_kernel(const float* raw, int 
 }
 
 // ---------------------------------------------------------------------------
-// The whole hyper-connection boundary of one row in one kernel: hc_post of
-// the previous sublayer's output (when y is given), the raw mixes
-// X_flat . fn^T in fp32 on the CUDA cores, the coefficients, and the next
-// sublayer's input RMSNorm(sum_c pre_c X_c) * w.  A row is split over the C
-// CTAs of a thread-block cluster, CTA r owning columns [r D/C, (r+1) D/C) of
-// every stream; the C partial mixes (and sums of squares) are summed in rank
-// order through distributed shared memory, so every CTA computes the same
-// coefficients.  Decode-sized batches: every row reads all of fn (M x 4D
-// fp32, from L2); long prefill chunks keep the tcgen05 stats GEMM.
-// Replaces hc_post + memset + stats GEMM + hc_pre (four launches).
-constexpr int kBThreads = 128;
+// The whole hyper-connection boundary in one kernel: hc_post of the previous
+// sublayer's output (when y is given), the raw mixes X_flat . fn^T in fp32 on
+// the CUDA cores, the coefficients, and the next sublayer's input
+// RMSNorm(sum_c pre_c X_c) * w.  A CTA owns kBRows rows and D / C columns of
+// every stream; the C CTAs of a thread-block cluster cover a row group's
+// columns and sum their partial mixes and sums of squares in rank order
+// through distributed shared memory, so every CTA derives the same
+// coefficients.  Each CTA reads its slice of fn (M x 4 x D/C fp32) once for
+// all kBRows rows: a warp takes three mix rows m, its lanes stride the slice
+// by float4, and every fn load feeds kBRows dot products against the rows
+// staged in shared memory.  Decode-sized batches; long prefill chunks keep
+// the tcgen05 stats GEMM.  Replaces hc_post + memset + stats GEMM + hc_pre
+// (four launches).  Sums run in fixed thread / warp / rank order.
+constexpr int kBThreads = 256;
+constexpr int kBWarps = kBThreads / 32;
+constexpr int kBRows = 8;          // rows per CTA (one warp each for the coefficients)
 constexpr int kBMaxM = 24;
+constexpr int kBMPerWarp = kBMaxM / kBWarps;   // 3
+static_assert(kBRows == kBWarps, "one warp per row for the coefficients");
 
 __global__ void __launch_bounds__(kBThreads) hc_boundary_kernel(
-    __nv_bfloat16* X, int D, int C, const __nv_bfloat16* y, int64_t ldy, const float* post_in, const float* comb_in,
-    const float* fn, int M, const float* scale, const float* base, int mode, int iters, float eps, float inv_width,
-    const float* norm_w, float norm_eps, float* post_out, float* comb_out, uint8_t* q, uint8_t* sf,
-    __nv_bfloat16* hb, float* hf) {
-  extern __shared__ __align__(16) float xs[];       // [kHC][Dq] this CTA's columns of the updated streams
-  __shared__ float part[kBMaxM + 2];                // raw mixes [M], sum sq of X, sum sq of h
-  __shared__ float wsum[kBThreads / 32][kBMaxM + 1];
-  __shared__ float tot[kBMaxM + 1];
-  __shared__ float cf[kHC * kHC + kHC];
-  __shared__ float pre_s[kHC];
-  __shared__ float red[32];
-  const int t = blockIdx.y;
+    __nv_bfloat16* X, int T, int D, int C, const __nv_bfloat16* y, int64_t ldy, const float* post_in,
+    const float* comb_in, const float* fn, int M, const float* scale, const float* base, int mode, int iters,
+    float eps, float inv_width, const float* norm_w, float norm_eps, float* post_out, float* comb_out, uint8_t* q,
+    uint8_t* sf, __nv_bfloat16* hb, float* hf) {
+  extern __shared__ __align__(16) float xs[];       // [kBRows][kHC][Dq] updated streams of this CTA's columns
+  __shared__ float part[kBRows][kBMaxM + 2];        // partial mixes [M], sum sq of X, sum sq of h
+  __shared__ float tot[kBRows][kBMaxM + 1];
+  __shared__ float wsum[kBWarps][kBRows];
+  __shared__ float cf[kBRows][kHC * kHC + kHC];
+  __shared__ float pre_s[kBRows][kHC];
+  __shared__ float rstd_s[kBRows];
   const int rank = int(cluster_ctarank());
   const int Dq = D / C, d0 = rank * Dq;
+  const int t0 = blockIdx.y * kBRows;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nit = (Dq + kBThreads * 8 - 1) / (kBThreads * 8);
+  const int vpr = Dq / 8;                          // 8-column vectors per row and stream
+  const int items = kBRows * vpr;
   pdl_wait();
   if (tid == 0) pdl_launch_dependents();
   if (y) {
-    if (tid < kHC * kHC) cf[tid] = __ldcg(comb_in + (int64_t)t * kHC * kHC + tid);
-    if (tid < kHC) cf[kHC * kHC + tid] = __ldcg(post_in + (int64_t)t * kHC + tid);
+    for (int i = tid; i < kBRows * (kHC * kHC + kHC); i += kBThreads) {
+      const int r = i / (kHC * kHC + kHC), j = i % (kHC * kHC + kHC), t = t0 + r;
+      cf[r][j] = t < T ? (j < kHC * kHC ? __ldcg(comb_in + (int64_t)t * kHC * kHC + j)
+                                        : __ldcg(post_in + (int64_t)t * kHC + j - kHC * kHC))
+                       : 0.f;
+    }
     __syncthreads();
   }
-  __nv_bfloat16* xt = X + (int64_t)t * kHC * D + d0;
-  // 1. hc_post on this CTA's columns (in place), streams kept in fp32 smem
-  float ssx = 0.f;
-  for (int it = 0; it < nit; ++it) {
-    const int v = (tid + it * kBThreads) * 8;
-    if (v >= Dq) break;
+  // 1. hc_post on this CTA's columns (in place); fp32 copies in shared memory
+  float ssx[kBRows];
+#pragma unroll
+  for (int r = 0; r < kBRows; ++r) ssx[r] = 0.f;
+  for (int i = tid; i < items; i += kBThreads) {
+    const int r = i / vpr, v = (i % vpr) * 8, t = t0 + r;
     float xr[kHC][8];
+    if (t < T) {
+      __nv_bfloat16* xt = X + (int64_t)t * kHC * D + d0;
 #pragma unroll
-    for (int r = 0; r < kHC; ++r) load8(xt + (int64_t)r * D + v, xr[r]);
-    if (y) {
-      float yv[8];
-      load8(y + (int64_t)t * ldy + d0 + v, yv);
-      float o[kHC][8];
+      for (int c = 0; c < kHC; ++c) load8(xt + (int64_t)c * D + v, xr[c]);
+      if (y) {
+        float yv[8], o[kHC][8];
+        load8(y + (int64_t)t * ldy + d0 + v, yv);
 #pragma unroll
-      for (int c = 0; c < kHC; ++c) {
+        for (int c = 0; c < kHC; ++c) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float a = cf[kHC * kHC + c] * yv[i];
+          for (int e = 0; e < 8; ++e) {
+            float a = cf[r][kHC * kHC + c] * yv[e];
 #pragma unroll
-          for (int r = 0; r < kHC; ++r) a = fmaf(cf[r * kHC + c], xr[r][i], a);
-          o[c][i] = bf16_round(a);
+            for (int rr = 0; rr < kHC; ++rr) a = fmaf(cf[r][rr * kHC + c], xr[rr][e], a);
+            o[c][e] = bf16_round(a);
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < kHC; ++c) {
+          store8_bf16(xt + (int64_t)c * D + v, o[c]);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) xr[c][e] = o[c][e];
         }
       }
+    } else {
 #pragma unroll
-      for (int c = 0; c < kHC; ++c) {
-        store8_bf16(xt + (int64_t)c * D + v, o[c]);
+      for (int c = 0; c < kHC; ++c)
 #pragma unroll
-        for (int i = 0; i < 8; ++i) xr[c][i] = o[c][i];
-      }
+        for (int e = 0; e < 8; ++e) xr[c][e] = 0.f;
     }
+    float s2 = 0.f;
 #pragma unroll
     for (int c = 0; c < kHC; ++c) {
+      float* dst = xs + ((int64_t)r * kHC + c) * Dq + v;
+      *reinterpret_cast<float4*>(dst) = make_float4(xr[c][0], xr[c][1], xr[c][2], xr[c][3]);
+      *reinterpret_cast<float4*>(dst + 4) = make_float4(xr[c][4], xr[c][5], xr[c][6], xr[c][7]);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        xs[c * Dq + v + i] = xr[c][i];
-        ssx = fmaf(xr[c][i], xr[c][i], ssx);
-      }
+      for (int e = 0; e < 8; ++e) s2 = fmaf(xr[c][e], xr[c][e], s2);
     }
-  }
-  // 2. partial raw mixes over this CTA's columns: fn row m, column c D + d
-  float acc[kBMaxM];
 #pragma unroll
-  for (int m = 0; m < kBMaxM; ++m) acc[m] = 0.f;
-  const int64_t K = (int64_t)kHC * D;
-  for (int it = 0; it < nit; ++it) {
-    const int v = (tid + it * kBThreads) * 8;
-    if (v >= Dq) break;
-#pragma unroll
-    for (int c = 0; c < kHC; ++c) {
-      float xv[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) xv[i] = xs[c * Dq + v + i];
-      const float* f = fn + (int64_t)c * D + d0 + v;
-#pragma unroll
-      for (int m = 0; m < kBMaxM; ++m) {
-        if (m < M) {
-          const float4 a = *reinterpret_cast<const float4*>(f + m * K);
-          const float4 b = *reinterpret_cast<const float4*>(f + m * K + 4);
-          acc[m] = fmaf(xv[0], a.x, fmaf(xv[1], a.y, fmaf(xv[2], a.z, fmaf(xv[3], a.w, acc[m]))));
-          acc[m] = fmaf(xv[4], b.x, fmaf(xv[5], b.y, fmaf(xv[6], b.z, fmaf(xv[7], b.w, acc[m]))));
-        }
-      }
-    }
+    for (int rr = 0; rr < kBRows; ++rr) ssx[rr] += (rr == r) ? s2 : 0.f;
   }
 #pragma unroll
-  for (int m = 0; m < kBMaxM; ++m) {
+  for (int r = 0; r < kBRows; ++r) {
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+    for (int o = 16; o > 0; o >>= 1) ssx[r] += __shfl_xor_sync(0xffffffffu, ssx[r], o);
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ssx += __shfl_xor_sync(0xffffffffu, ssx, o);
   if (lane == 0) {
 #pragma unroll
-    for (int m = 0; m < kBMaxM; ++m) wsum[warp][m] = acc[m];
-    wsum[warp][kBMaxM] = ssx;
+    for (int r = 0; r < kBRows; ++r) wsum[warp][r] = ssx[r];
   }
   __syncthreads();
-  if (tid <= kBMaxM) {
+  if (tid < kBRows) {
     float a = 0.f;
-#pragma unroll
-    for (int w = 0; w < kBThreads / 32; ++w) a += wsum[w][tid];
-    part[tid] = a;
+    for (int w = 0; w < kBWarps; ++w) a += wsum[w][tid];
+    part[tid][kBMaxM] = a;
   }
-  // 3. the cluster's partials, summed in rank order (the same in every CTA)
-  cluster_sync();
-  if (tid <= kBMaxM) {
-    const uint32_t a = smem_u32(&part[tid]);
-    float s = 0.f;
-    for (int r = 0; r < C; ++r) s += ld_dsmem_f32(mapa_shared(a, r));
-    tot[tid] = s;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    const float rs = 1.f / sqrtf(tot[kBMaxM] * inv_width + eps);
-    const bool w0 = rank == 0 && mode == 0;
-    hc_coeffs_warp([&](int j) { return tot[j]; }, rs, scale, base, mode, iters, eps, pre_s,
-                   w0 ? post_out + (int64_t)t * kHC : nullptr, w0 ? comb_out + (int64_t)t * kHC * kHC : nullptr);
-  }
-  __syncthreads();
-  // 4. h = sum_c pre_c X_c on this CTA's columns; its sum of squares over the cluster
-  float p[kHC];
+  // 2. partial mixes: warp w takes m = w, w + 8, w + 16; lanes stride the
+  // CTA's 4 x Dq columns by float4; each fn load serves all kBRows rows
+  {
+    float acc[kBMPerWarp][kBRows];
 #pragma unroll
-  for (int c = 0; c < kHC; ++c) p[c] = pre_s[c];
-  float ssh = 0.f;
-  for (int it = 0; it < nit; ++it) {
-    const int v = (tid + it * kBThreads) * 8;
-    if (v >= Dq) break;
+    for (int j = 0; j < kBMPerWarp; ++j)
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float h = 0.f;
+      for (int r = 0; r < kBRows; ++r) acc[j][r] = 0.f;
+    const int64_t K = (int64_t)kHC * D;
+    const int ks = kHC * Dq;
+    for (int k = lane * 4; k < ks; k += 128) {
+      const int c = k / Dq, d = k % Dq;            // Dq % 4 == 0: a float4 never straddles streams
+      const float* f = fn + (int64_t)c * D + d0 + d;
+      float4 fw[kBMPerWarp];
 #pragma unroll
-      for (int c = 0; c < kHC; ++c) h = fmaf(p[c], xs[c * Dq + v + i], h);
-      ssh = fmaf(h, h, ssh);
+      for (int j = 0; j < kBMPerWarp; ++j) {
+        const int m = warp + j * kBWarps;
+        fw[j] = m < M ? *reinterpret_cast<const float4*>(f + m * K) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int r = 0; r < kBRows; ++r) {
+        const float4 xv = *reinterpret_cast<const float4*>(xs + ((int64_t)r * kHC + c) * Dq + d);
+#pragma unroll
+        for (int j = 0; j < kBMPerWarp; ++j)
+          acc[j][r] = fmaf(xv.x, fw[j].x, fmaf(xv.y, fw[j].y, fmaf(xv.z, fw[j].z, fmaf(xv.w, fw[j].w, acc[j][r]))));
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kBMPerWarp; ++j) {
+#pragma unroll
+      for (int r = 0; r < kBRows; ++r) {
+        float a = acc[j][r];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        const int m = warp + j * kBWarps;
+        if (lane == 0 && m < M) part[r][m] = a;
+      }
     }
   }
-  ssh = block_sum(ssh, red);
-  if (tid == 0) part[kBMaxM + 1] = ssh;
+  // 3. the cluster's partials summed in rank order (the same in every CTA)
   cluster_sync();
-  if (tid == 0) {
-    const uint32_t a = smem_u32(&part[kBMaxM + 1]);
-    float s = 0.f;
-    for (int r = 0; r < C; ++r) s += ld_dsmem_f32(mapa_shared(a, r));
-    red[0] = s;
+  for (int i = tid; i < kBRows * (kBMaxM + 1); i += kBThreads) {
+    const int r = i / (kBMaxM + 1), j = i % (kBMaxM + 1);
+    if (j < M || j == kBMaxM) {
+      const uint32_t a = smem_u32(&part[r][j]);
+      float sum = 0.f;
+      for (int rr = 0; rr < C; ++rr) sum += ld_dsmem_f32(mapa_shared(a, rr));
+      tot[r][j] = sum;
+    }
+  }
+  __syncthreads();
+  {
+    const int r = warp, t = t0 + r;               // one warp per row (kBRows == kBWarps)
+    if (t < T) {
+      const float rs = 1.f / sqrtf(tot[r][kBMaxM] * inv_width + eps);
+      const bool w0 = rank == 0 && mode == 0;
+      hc_coeffs_warp([&](int j) { return tot[r][j]; }, rs, scale, base, mode, iters, eps, pre_s[r],
+                     w0 ? post_out + (int64_t)t * kHC : nullptr, w0 ? comb_out + (int64_t)t * kHC * kHC : nullptr);
+    } else if (lane < kHC) {
+      pre_s[r][lane] = 0.f;
+    }
+  }
+  __syncthreads();
+  // 4. h = sum_c pre_c X_c on this CTA's columns; per-row sums of squares over the cluster
+  float ssh[kBRows];
+#pragma unroll
+  for (int r = 0; r < kBRows; ++r) ssh[r] = 0.f;
+  for (int i = tid; i < items; i += kBThreads) {
+    const int r = i / vpr, v = (i % vpr) * 8;
+    float s2 = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float h = 0.f;
+#pragma unroll
+      for (int c = 0; c < kHC; ++c) h = fmaf(pre_s[r][c], xs[((int64_t)r * kHC + c) * Dq + v + e], h);
+      s2 = fmaf(h, h, s2);
+    }
+#pragma unroll
+    for (int rr = 0; rr < kBRows; ++rr) ssh[rr] += (rr == r) ? s2 : 0.f;
+  }
+#pragma unroll
+  for (int r = 0; r < kBRows; ++r) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ssh[r] += __shfl_xor_sync(0xffffffffu, ssh[r], o);
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int r = 0; r < kBRows; ++r) wsum[warp][r] = ssh[r];
+  }
+  __syncthreads();
+  if (tid < kBRows) {
+    float a = 0.f;
+    for (int w = 0; w < kBWarps; ++w) a += wsum[w][tid];
+    part[tid][kBMaxM + 1] = a;
+  }
+  cluster_sync();
+  if (tid < kBRows) {
+    const uint32_t a = smem_u32(&part[tid][kBMaxM + 1]);
+    float sum = 0.f;
+    for (int rr = 0; rr < C; ++rr) sum += ld_dsmem_f32(mapa_shared(a, rr));
+    rstd_s[tid] = 1.f / sqrtf(sum / D + norm_eps);
   }
   // the last reads of other CTAs' shared memory are done after this barrier
   cluster_sync();
-  const float rstd = 1.f / sqrtf(red[0] / D + norm_eps);
+  // 5. RMSNorm * w -> bf16 / fp32 / MXFP8.  A uniform trip count: quant8's
+  // 4-lane amax exchange needs the whole warp; vpr % 4 == 0 keeps a 32-column
+  // block's four lanes on one row.
   const int kb = D / 32;
-  // 5. RMSNorm * w -> bf16 / fp32 / MXFP8 (a uniform trip count: quant8's
-  // 4-lane amax exchange needs the whole warp)
+  const int nit = (items + kBThreads - 1) / kBThreads;
   for (int it = 0; it < nit; ++it) {
-    const int v = (tid + it * kBThreads) * 8;
-    const bool ok = v < Dq;
-    float yv[8], w[8];
+    const int i = it * kBThreads + tid;
+    const int r = i / vpr, v = (i % vpr) * 8, t = t0 + r;
+    const bool ok = i < items && t < T;
+    float yv[8];
     if (ok) {
-      load8(norm_w + d0 + v, w);
+      float w8[8];
+      load8(norm_w + d0 + v, w8);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int e = 0; e < 8; ++e) {
         float h = 0.f;
 #pragma unroll
-        for (int c = 0; c < kHC; ++c) h = fmaf(p[c], xs[c * Dq + v + i], h);
-        yv[i] = h * rstd * w[i];
+        for (int c = 0; c < kHC; ++c) h = fmaf(pre_s[r][c], xs[((int64_t)r * kHC + c) * Dq + v + e], h);
+        yv[e] = h * rstd_s[r] * w8[e];
       }
       if (hb) store8_bf16(hb + (int64_t)t * D + d0 + v, yv);
       if (hf) store8_f32(hf + (int64_t)t * D + d0 + v, yv);
     } else {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) yv[i] = 0.f;
+      for (int e = 0; e < 8; ++e) yv[e] = 0.f;
     }
-    if (q) quant8(yv, q + (int64_t)t * D + d0 + v, sf, t, d0 + v, kb, ok);
+    if (q) quant8(yv, q + (int64_t)(ok ? t : 0) * D + d0 + v, sf, ok ? t : 0, d0 + v, kb, ok);
   }
 }
 
@@ -1010,17 +1067,18 @@ int b200_hc_boundary(void* X, int T, int hc, int D, const void* y, int64_t ldy, 
   if (T <= 0) return 0;
   if (hc != kHC || M > kBMaxM || M < kHC || (mode == 0 && (!post || !comb || M < 2 * kHC + kHC * kHC))) return -1;
   if (y && (!post_in || !comb_in)) return -1;
+  // C CTAs per row group: columns per CTA a multiple of 32 (quant blocks on
+  // one CTA, whole float4s per stream), the rows' fp32 copies in shared memory
   int C = 0;
   for (int c = 8; c >= 1; c >>= 1)
-    if (D % (32 * c) == 0 && D / c >= 128) { C = c; break; }
-  if (C == 0 || D % 8 || (reinterpret_cast<uintptr_t>(fn) & 15)) return -2;
+    if (D % (32 * c) == 0 && size_t(kBRows) * kHC * (D / c) * sizeof(float) <= 160 * 1024) { C = c; break; }
+  if (C == 0 || (reinterpret_cast<uintptr_t>(fn) & 15)) return -2;
   const int Dq = D / C;
-  const size_t smem = size_t(kHC) * Dq * sizeof(float);
-  if (smem > 200 * 1024) return -3;
+  const size_t smem = size_t(kBRows) * kHC * Dq * sizeof(float);
   auto kern = hc_boundary_kernel;
   if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(C, T);
+  cfg.gridDim = dim3(C, (T + kBRows - 1) / kBRows);
   cfg.blockDim = dim3(kBThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -1033,7 +1091,7 @@ int b200_hc_boundary(void* X, int T, int hc, int D, const void* y, int64_t ldy, 
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = b200::pdl_enabled() ? 2 : 1;
-  const cudaError_t err = cudaLaunchKernelEx(&cfg, kern, reinterpret_cast<__nv_bfloat16*>(X), D, C,
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kern, reinterpret_cast<__nv_bfloat16*>(X), T, D, C,
                                              reinterpret_cast<const __nv_bfloat16*>(y), ldy, post_in, comb_in, fn, M,
                                              scale, base, mode, iters, eps, inv_width, norm_w, norm_eps, post, comb, q,
                                              sf, reinterpret_cast<__nv_bfloat16*>(hb), hf);
