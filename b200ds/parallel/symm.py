@@ -86,18 +86,29 @@ class FusedAllReduce:
         y = torch.empty(T, H, dtype=torch.bfloat16, device=a.device) if (keep_bf16 or not quantize) else None
         qa = alloc_qact(T, H, a.device) if quantize else None
         if self._one_kernel():
-            _C.ar_fused_norm(x, None, None, T, self.bases, self.rank, self.max_tokens, self.epoch, self.ticket,
-                             residual, w, eps, y, qa.q if qa else None, qa.sf if qa else None, self.err)
+            self._fused(x, None, None, T, residual, w, eps, y, qa)
             return self._done(y, qa, residual)
         bases, epoch, ticket, mc = self._push_target()
         _C.ar_push(x, bases, self.rank, self.max_tokens, epoch, ticket, self.push_ctas, mc=mc)
         return self._reduce(T, H, 1, residual, w, eps, y, qa)
 
     def _one_kernel(self) -> bool:
-        """Push, per-CTA arrivals and reduce + norm in one launch (push mode;
-        the NVLS path keeps its two kernels)."""
+        """Push, per-CTA arrivals and reduce + norm in one launch: the push
+        protocol (switch `ar_one_kernel`) or, on NVLS groups, the variant
+        whose rows are summed through the switch by one rank per CTA (switch
+        `nvls_one_kernel`; otherwise NVLS keeps push + reduce kernels)."""
         from ..utils import levers
-        return self.nvls is None and levers.on("ar_one_kernel")
+        if self.nvls is None:
+            return levers.on("ar_one_kernel")
+        return levers.on("nvls_one_kernel")
+
+    def _fused(self, x, pair_row, add, T, residual, w, eps, y, qa):
+        from .. import _C
+        n = self.nvls
+        bases, epoch, ticket, mc = (n.bases, n.epoch, n.ticket, n.mc) if n is not None else \
+            (self.bases, self.epoch, self.ticket, 0)
+        _C.ar_fused_norm(x, pair_row, add, T, bases, self.rank, self.max_tokens, epoch, ticket, residual, w, eps, y,
+                         qa.q if qa else None, qa.sf if qa else None, self.err, mc=mc)
 
     @staticmethod
     def _done(y, qa, residual):
@@ -154,8 +165,7 @@ class FusedAllReduce:
         add = part.add.to(torch.bfloat16).contiguous() if part.add is not None else None
         if self._one_kernel():
             y, qa = self._outs(T, H, part.y.device, quantize)
-            _C.ar_fused_norm(part.y, part.pair_row, add, T, self.bases, self.rank, self.max_tokens, self.epoch,
-                             self.ticket, residual, ln_w, eps, y, qa.q if qa else None, qa.sf if qa else None, self.err)
+            self._fused(part.y, part.pair_row, add, T, residual, ln_w, eps, y, qa)
             return self._done(y, qa, residual)
         bases, epoch, ticket, mc = self._push_target()
         _C.moe_combine_push(part.y, part.pair_row, add, bases, self.rank, self.max_tokens, epoch, ticket,

@@ -132,6 +132,9 @@ register("ep_combine_epilogue", "B200_EP_COMBINE_EPILOGUE", True,
 register("ar_one_kernel", "B200_AR_ONE_KERNEL", True,
          "push-mode all-reduces (and the TP MoE combine) run push + per-CTA arrivals + reduce + norm as one kernel "
          "instead of a push kernel and a reduce kernel")
+register("nvls_one_kernel", "B200_NVLS_ONE_KERNEL", False,
+         "NVLS groups: one kernel per all-reduce - each CTA's rows stored locally, summed through the switch by "
+         "rank c % world and broadcast back, per-CTA flags (off: push kernel + NVLS reduce kernel)")
 register("hc_boundary", "B200_HC_BOUNDARY", False,
          "V4 family, decode-sized batches: hc_post + the mHC mixes (fp32, CUDA cores) + coefficients + the next "
          "sublayer's normed input as one kernel, a thread-block cluster per row")

@@ -15,6 +15,8 @@ o_proj GEMM + all-reduce (bf16 partial [M, 7168], K = 16384 / N):
   * push_ar        our one-shot NVLink push + reduce (+residual +RMSNorm
                    +MXFP8) as one kernel (per-CTA arrivals);
   * push2_ar       the same as a push kernel + a reduce kernel;
+  * nvls1_ar       one-kernel NVLS variant (rows stored locally, summed
+                   through the switch by one rank per CTA, broadcast back);
   * nvls_ar        the same through NVLink multicast (multimem.ld_reduce /
                    multimem.st in the switch), when the GPUs support it;
   * gemm_nccl      our MXFP8 GEMM + NCCL all-reduce;
@@ -142,6 +144,9 @@ def ar_part(ps, Ms):
         levers.set_switch("ar_one_kernel", True)
         if far_nvls is not None:
             res["nvls_ar_us"] = timed(lambda: far_nvls.allreduce_add_rmsnorm(part, resid, ln, 1e-6, True), iters)
+            levers.set_switch("nvls_one_kernel", True)
+            res["nvls1_ar_us"] = timed(lambda: far_nvls.allreduce_add_rmsnorm(part, resid, ln, 1e-6, True), iters)
+            levers.set_switch("nvls_one_kernel", False)
         res["gemm_nccl_us"] = timed(lambda: dist.all_reduce(oc.gemm(x, w)), iters)
         if M <= 128:
             res["gemm_push_us"] = timed(lambda: far_push.gemm_allreduce_add_rmsnorm(x, w, resid, ln, 1e-6, True),
@@ -164,7 +169,7 @@ def ar_part(ps, Ms):
         fused = [res.get(k) for k in ("gemm_nvls_us", "gemm_push_us") if res.get(k)]
         best = min(fused) if fused else min(v for v in (res.get("gemm_nccl_us"),) if v)
         res["fused_gemm_ar_fraction_of_roofline"] = res["roofline_us"] / best
-        ars = [res.get(k) for k in ("nvls_ar_us", "push_ar_us") if res.get(k)]
+        ars = [res.get(k) for k in ("nvls_ar_us", "nvls1_ar_us", "push_ar_us") if res.get(k)]
         res["fused_ar_fraction_of_roofline"] = res["ar_roofline_us"] / min(ars) if ars else None
         res["peaks"] = PEAK_SRC
         for f in (far_push, far_nvls):

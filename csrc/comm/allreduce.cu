@@ -535,6 +535,155 @@ __global__ void __launch_bounds__(kThreads) nvls_ar_norm_kernel(
   }
 }
 
+// One-kernel NVLS all-reduce (+ MoE combine) + residual + RMSNorm (+ MXFP8).
+// CTA c of G owns rows c, c + G, ... on every rank and rank c % world
+// reduces them: every rank's CTA c stores its rows' partial into its own
+// in[p] (local stores), raises cta_cnt[p][c] on the reducer; the reducer's
+// CTA c waits for all world arrivals, sums the rows through the switch
+// (multimem.ld_reduce over in[p]) and broadcasts the sums into every rank's
+// out[p] (multimem.st), then raises cta_cnt2[p][c] on every rank; every
+// rank's CTA c waits for that flag and runs the row epilogue on out[p].
+// Only per-CTA flags, one launch; each rank's memory is read once per row
+// through the switch and the sums cross NVLink once.  The last CTA (ticket)
+// zeroes this parity's flags and advances the epoch.
+template <bool COMBINE>
+__global__ void __launch_bounds__(kThreads) nvls_fused_norm_kernel(
+    const __nv_bfloat16* __restrict__ x, const int* __restrict__ pair_row, int K, const __nv_bfloat16* __restrict__ add,
+    int T, int hidden, ArPeers peers, uint32_t* epoch, uint32_t* ticket, float* residual, const float* __restrict__ w,
+    float eps, __nv_bfloat16* y, uint8_t* q, uint8_t* sf, uint32_t* err) {
+  __shared__ float red[32];
+  __shared__ int ok_s;
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  const int p = (*epoch) & 1;
+  const int G = gridDim.x, c = blockIdx.x;
+  const int reducer = c % peers.world;
+  uint8_t* mine = peers.base[peers.rank];
+  const int64_t slot = (int64_t)peers.max_t * hidden;                 // elements per slot
+  const int64_t in_off = kArRecvOff + (int64_t)p * slot * 2;           // bytes
+  const int64_t out_off = kArRecvOff + (int64_t)(2 + p) * slot * 2;
+  const int units = hidden >> 3;
+  __nv_bfloat16* in_mine = reinterpret_cast<__nv_bfloat16*>(mine + in_off);
+  // 1. this CTA's rows of the partial into this rank's own input slot
+  for (int t = c; t < T; t += G) {
+    for (int u = threadIdx.x; u < units; u += kThreads) {
+      uint4 outv;
+      if constexpr (COMBINE) {
+        float acc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+        for (int j = 0; j < K; ++j) {
+          const int r = __ldcg(pair_row + t * K + j);
+          if (r < 0) continue;
+          const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(x + (int64_t)r * hidden) + u);
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h[i]);
+            acc[2 * i] += f.x;
+            acc[2 * i + 1] += f.y;
+          }
+        }
+        if (add) {
+          const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(add + (int64_t)t * hidden) + u);
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h[i]);
+            acc[2 * i] += f.x;
+            acc[2 * i + 1] += f.y;
+          }
+        }
+        __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&outv);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+      } else {
+        outv = __ldcg(reinterpret_cast<const uint4*>(x + (int64_t)t * hidden) + u);
+      }
+      *reinterpret_cast<uint4*>(in_mine + (int64_t)t * hidden + u * 8) = outv;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(cta_counters(peers.base[reducer], p) + c), "r"(1u)
+                 : "memory");
+  }
+  // 2. the reducer sums the rows through the switch and broadcasts them
+  int ok = 1;
+  if (peers.rank == reducer) {
+    if (threadIdx.x == 0) {
+      const uint32_t* cnt = cta_counters(mine, p) + c;
+      const uint64_t t0 = globaltimer_ns();
+      while (ld_acquire_sys(cnt) < (uint32_t)peers.world) {
+        if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+          atomicExch(err, kErrPeerTimeout);
+          ok = 0;
+          break;
+        }
+      }
+      ok_s = ok;
+    }
+    __syncthreads();
+    ok = ok_s;
+    if (ok) {
+      const uint4* in_mc = reinterpret_cast<const uint4*>(peers.mc + in_off);
+      uint4* out_mc = reinterpret_cast<uint4*>(peers.mc + out_off);
+      for (int t = c; t < T; t += G)
+        for (int u = threadIdx.x; u < units; u += kThreads) {
+          const int64_t v = (int64_t)t * units + u;
+          uint4 s;
+          mm_ld_reduce_bf16x8(in_mc + v, s);
+          mm_st_b128(out_mc + v, s);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && ok) {
+      __threadfence_system();
+      for (int d = 0; d < peers.world; ++d)
+        asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(cta_counters2(peers.base[d], p) + c), "r"(1u)
+                     : "memory");
+    }
+  }
+  // 3. wait for this CTA's broadcast rows, then the row epilogue
+  if (threadIdx.x == 0) {
+    int ok2 = 1;
+    const uint32_t* cnt = cta_counters2(mine, p) + c;
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_sys(cnt) < 1u) {
+      if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+        atomicExch(err, kErrPeerTimeout);
+        ok2 = 0;
+        break;
+      }
+    }
+    ok_s = ok2;
+  }
+  __syncthreads();
+  if (ok_s)
+    for (int t = c; t < T; t += G) {
+      row_add_norm_quant(t, hidden, reinterpret_cast<const __nv_bfloat16*>(mine + out_off), 0, 1, hidden, nullptr,
+                         nullptr, residual, w, eps, y, q, sf, red);
+      __syncthreads();
+    }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t tk = atomicAdd(ticket, 1u);
+    if (tk == (uint32_t)G - 1) {
+      uint32_t* c1 = cta_counters(mine, p);
+      uint32_t* c2 = cta_counters2(mine, p);
+      for (int i = 0; i < G; ++i) {
+        atomicExch(c1 + i, 0u);
+        atomicExch(c2 + i, 0u);
+      }
+      *ticket = 0u;
+      __threadfence();
+      atomicAdd(epoch, 1u);
+    }
+  }
+}
+
 }  // namespace comm
 }  // namespace b200
 
@@ -613,13 +762,23 @@ int b200_ar_fused_norm(const void* x, const int* pair_row, int K, const void* ad
                        const ArPeers* peers, uint32_t* epoch, uint32_t* ticket, float* residual, const float* w,
                        float eps, void* y, uint8_t* q, uint8_t* sf, uint32_t* err, cudaStream_t st) {
   if (T <= 0) return 0;
-  if (T > peers->max_t || hidden % 32 || hidden > b200::comm::kThreads * 8 * b200::comm::kMaxIt || peers->mc ||
+  if (T > peers->max_t || hidden % 32 || hidden > b200::comm::kThreads * 8 * b200::comm::kMaxIt ||
       (pair_row && K <= 0))
     return -1;
   const int G = std::min(T, std::min(148, kArMaxCtas));
   const auto* xb = reinterpret_cast<const __nv_bfloat16*>(x);
   const auto* ab = reinterpret_cast<const __nv_bfloat16*>(add);
   auto* yb = reinterpret_cast<__nv_bfloat16*>(y);
+  if (peers->mc) {
+    if (pair_row)
+      b200::launch_pdl(b200::comm::nvls_fused_norm_kernel<true>, dim3(G), dim3(b200::comm::kThreads), 0, st, xb,
+                       pair_row, K, ab, T, hidden, *peers, epoch, ticket, residual, w, eps, yb, q, sf, err);
+    else
+      b200::launch_pdl(b200::comm::nvls_fused_norm_kernel<false>, dim3(G), dim3(b200::comm::kThreads), 0, st, xb,
+                       (const int*)nullptr, 0, (const __nv_bfloat16*)nullptr, T, hidden, *peers, epoch, ticket,
+                       residual, w, eps, yb, q, sf, err);
+    return cudaGetLastError() == cudaSuccess ? 0 : 1;
+  }
   if (pair_row)
     b200::launch_pdl(b200::comm::ar_fused_norm_kernel<true>, dim3(G), dim3(b200::comm::kThreads), 0, st, xb, pair_row,
                      K, ab, T, hidden, *peers, epoch, ticket, residual, w, eps, yb, q, sf, err);

@@ -6,11 +6,13 @@
 constexpr int kArMaxRanks = 8;
 // Push all-reduce buffer: [0, 64) uint32 cnt[2][kArMaxRanks] (per-source
 // arrivals), [128, 192) NVLS cnt2, [kArCtaCntOff, +2 KB) uint32
-// cta_cnt[2][kArMaxCtas] (per-CTA arrivals of the one-kernel all-reduce),
-// then the receive slots from kArRecvOff.
+// cta_cnt[2][kArMaxCtas] (per-CTA arrivals of the one-kernel all-reduces),
+// [kArCtaCnt2Off, +2 KB) cta_cnt2[2][kArMaxCtas] (per-CTA "sum broadcast" of
+// the one-kernel NVLS variant), then the receive slots from kArRecvOff.
 constexpr int kArMaxCtas = 256;
 constexpr int64_t kArCtaCntOff = 256;
-constexpr int64_t kArRecvOff = 4096;
+constexpr int64_t kArCtaCnt2Off = kArCtaCntOff + 2 * kArMaxCtas * 4;
+constexpr int64_t kArRecvOff = 8192;
 
 // Symmetric-buffer base pointers of every rank (UVA peer mappings).
 struct ArPeers {
@@ -58,7 +60,11 @@ int b200_ar_reduce_norm(int T, int hidden, const ArPeers* peers, uint32_t* epoch
                         cudaStream_t st);
 // One kernel: push (plain partial x, or with pair_row the MoE combine of the
 // local expert rows y + add) + per-CTA arrivals + reduce + residual +
-// RMSNorm (+ MXFP8) of the rows each CTA owns.  Push mode only (no NVLS).
+// RMSNorm (+ MXFP8) of the rows each CTA owns.  With peers->mc (the NVLS
+// buffer's multicast address) CTA c stores its rows only into this rank's
+// own input slot, rank c % world sums them through the switch
+// (multimem.ld_reduce) and broadcasts the sum (multimem.st), and every
+// rank's CTA c normalises the broadcast rows.
 int b200_ar_fused_norm(const void* x, const int* pair_row, int K, const void* add, int T, int hidden,
                        const ArPeers* peers, uint32_t* epoch, uint32_t* ticket, float* residual, const float* w,
                        float eps, void* y, uint8_t* q, uint8_t* sf, uint32_t* err, cudaStream_t st);

@@ -70,7 +70,7 @@ void moe_combine_push(const at::Tensor& y, const at::Tensor& pair_row, c10::opti
 void ar_fused_norm(const at::Tensor& x, c10::optional<at::Tensor> pair_row, c10::optional<at::Tensor> add, int64_t T,
                    std::vector<int64_t> bases, int64_t rank, int64_t max_t, at::Tensor epoch, at::Tensor ticket,
                    at::Tensor residual, const at::Tensor& w, double eps, c10::optional<at::Tensor> y,
-                   c10::optional<at::Tensor> q, c10::optional<at::Tensor> sf, at::Tensor err) {
+                   c10::optional<at::Tensor> q, c10::optional<at::Tensor> sf, at::Tensor err, int64_t mc) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() == 2, "x bf16 rows");
   TORCH_CHECK(residual.scalar_type() == at::kFloat && residual.is_contiguous(), "residual fp32");
   const bool comb = pair_row.has_value() && pair_row->defined();
@@ -84,7 +84,7 @@ void ar_fused_norm(const at::Tensor& x, c10::optional<at::Tensor> pair_row, c10:
     TORCH_CHECK(add->scalar_type() == at::kBFloat16 && add->is_contiguous(), "add bf16 [T, H]");
   }
   const c10::cuda::CUDAGuard g(x.device());
-  ArPeers p = make_peers(bases, rank, max_t);
+  ArPeers p = make_peers(bases, rank, max_t, mc);
   const int rc = b200_ar_fused_norm(x.data_ptr(), comb ? reinterpret_cast<const int*>(pair_row->data_ptr()) : nullptr,
                                     comb ? pair_row->size(1) : 0, optr<void>(add), T, x.size(1), &p,
                                     reinterpret_cast<uint32_t*>(epoch.data_ptr()),
@@ -300,7 +300,11 @@ void register_comm(pybind11::module& m) {
   m.def("ar_push", &ar_push, pybind11::arg("x"), pybind11::arg("bases"), pybind11::arg("rank"), pybind11::arg("max_t"),
         pybind11::arg("epoch"), pybind11::arg("ticket"), pybind11::arg("nctas"), pybind11::arg("mc") = 0);
   m.def("ar_reduce_norm", &ar_reduce_norm);
-  m.def("ar_fused_norm", &ar_fused_norm);
+  m.def("ar_fused_norm", &ar_fused_norm, pybind11::arg("x"), pybind11::arg("pair_row"), pybind11::arg("add"),
+        pybind11::arg("T"), pybind11::arg("bases"), pybind11::arg("rank"), pybind11::arg("max_t"),
+        pybind11::arg("epoch"), pybind11::arg("ticket"), pybind11::arg("residual"), pybind11::arg("w"),
+        pybind11::arg("eps"), pybind11::arg("y"), pybind11::arg("q"), pybind11::arg("sf"), pybind11::arg("err"),
+        pybind11::arg("mc") = 0);
   m.def("ar_buffer_size", &ar_buffer_size);
   m.def("nvls_buffer_size", &nvls_buffer_size);
   m.def("nvls_ar_norm", &nvls_ar_norm);

@@ -41,6 +41,10 @@ __device__ __forceinline__ uint32_t* cta_counters(uint8_t* base, int parity) {
   return reinterpret_cast<uint32_t*>(base + kArCtaCntOff) + parity * kArMaxCtas;
 }
 
+__device__ __forceinline__ uint32_t* cta_counters2(uint8_t* base, int parity) {
+  return reinterpret_cast<uint32_t*>(base + kArCtaCnt2Off) + parity * kArMaxCtas;
+}
+
 __device__ __forceinline__ uint32_t* counters2(uint8_t* base, int parity) {
   return reinterpret_cast<uint32_t*>(base + kNvlsCnt2Off) + parity * kArMaxRanks;
 }
