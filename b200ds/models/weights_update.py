@@ -62,9 +62,10 @@ def copy_weights(dst_model, src_model) -> int:
                                  f"the model holds {tuple(d.shape)} {d.dtype}")
             d.copy_(s)
             n += d.numel() * d.element_size()
-    try:
-        from ..ops import cuda as _cuda
-        _cuda._GATE_BF16.clear()
-    except ImportError:
-        pass
+            # derived copies kept on a weight (the router's bf16 gate) are
+            # refreshed in place: captured decode graphs read their buffers
+            hit = getattr(d, "_b200_bf16", None)
+            if hit is not None:
+                hit[1].copy_(d)
+                hit[0] = d._version
     return n

@@ -311,16 +311,24 @@ def _mla_core(q8, qs, cache, kv_scale, fb, softmax_scale, page_size, topk, lse_o
 
 
 # ---------------------------------------------------------------------------
-_GATE_BF16 = {}
+def _gate_bf16(gate: torch.Tensor) -> torch.Tensor:
+    """bf16 copy of a router gate, kept on the gate tensor itself (it lives
+    and dies with the weights; an in-place weight update bumps the tensor's
+    version and refreshes it)."""
+    hit = getattr(gate, "_b200_bf16", None)
+    if hit is None or hit[1].shape != gate.shape:
+        hit = [gate._version, gate.to(torch.bfloat16).contiguous()]
+        gate._b200_bf16 = hit
+    elif hit[0] != gate._version:
+        hit[1].copy_(gate)            # same buffer: captured decode graphs read the new values
+        hit[0] = gate._version
+    return hit[1]
 
 
 def router(x: torch.Tensor, gate: torch.Tensor, bias: torch.Tensor, cfg):
     """Router logits on the tensor cores (bf16 inputs, fp32 accumulate and
     output), then the fused sigmoid / group-limited top-k kernel."""
-    g16 = _GATE_BF16.get(gate.data_ptr())
-    if g16 is None or g16.shape != gate.shape:
-        g16 = gate.to(torch.bfloat16).contiguous()
-        _GATE_BF16[gate.data_ptr()] = g16
+    g16 = _gate_bf16(gate)
     xb = x.to(torch.bfloat16)
     T = xb.shape[0]
     E, Kd = g16.shape
