@@ -474,6 +474,9 @@ def sample_tokens(local_logits: torch.Tensor, vocab_off: int, temperature, top_p
 def sample(logits: torch.Tensor, temperature, top_p, top_k, uniform) -> torch.Tensor:
     if _use_native(logits):
         return _native().sample(logits, temperature, top_p, top_k, uniform)
+    if _use_baseline(logits):
+        from . import baseline
+        return baseline.sample_torch(logits, temperature, top_p, top_k, uniform)
     return ref.sample(logits, temperature, top_p, top_k, uniform)
 
 

@@ -373,3 +373,27 @@ if __name__ == "__main__":
     if len(sys.argv) > 1 and sys.argv[1] == "prebuild":
         root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
         prebuild_flashinfer(sys.argv[2] if len(sys.argv) > 2 else os.path.join(root, "baseline", "_fi"))
+
+
+def sample_torch(logits: torch.Tensor, temperature, top_p, top_k, uniform) -> torch.Tensor:
+    """Batched sampling in PyTorch ops (no host synchronisation): greedy rows
+    (temperature <= 0) take the argmax; the others draw from softmax(logits /
+    temperature) restricted to top-k (<= 0: off) and top-p, by inverse CDF at
+    the row's given uniform - the semantics of ref.sample."""
+    T, V = logits.shape
+    x = logits.float()
+    t = temperature.float().clamp(min=1e-6).unsqueeze(1)
+    p = (x / t).softmax(-1)
+    sp, si = p.sort(-1, descending=True)
+    ar = torch.arange(V, device=x.device).unsqueeze(0)
+    k = top_k.long().unsqueeze(1)
+    keep = (k <= 0) | (ar < k)
+    c = sp.cumsum(-1)
+    keep &= (c - sp) < top_p.float().unsqueeze(1)
+    sp = sp * keep
+    c = sp.cumsum(-1)
+    u = uniform.float().unsqueeze(1) * c[:, -1:]
+    j = torch.searchsorted(c, u).clamp(max=V - 1)
+    tok = si.gather(1, j).squeeze(1)
+    return torch.where(temperature.reshape(-1) <= 0, x.argmax(-1), tok)
+

@@ -255,7 +255,17 @@ def main():
 
     # ---- capture + warmup --------------------------------------------------------
     log(f"prefill done ({ttft_ms:.0f} ms); capturing decode graph")
-    eng.graphs.capture_all()
+    from b200ds.engine.cuda_graph import GraphCaptureFailed
+    graphs_ok = True
+    try:
+        eng.graphs.capture_all()
+    except GraphCaptureFailed as e:
+        # the library arm's PyTorch ops may not be capturable: it then runs
+        # (and is timed as) eager decode steps; our own arm must capture
+        if args.impl == "native":
+            raise
+        graphs_ok = False
+        eng._graphs_off("decode", e)
     log("warmup")
     for _ in range(args.warmup):
         eng.step()
@@ -272,7 +282,7 @@ def main():
     # on the context length only).
     points = context_points(args.input_len, args.output_len, args.steps, args.warmup)
     shares = [args.steps // len(points) + (1 if k < args.steps % len(points) else 0) for k in range(len(points))]
-    gr = eng.graphs.graphs[eng.graphs._bucket(len(eng.sched.running))]
+    gr = eng.graphs.graphs[eng.graphs._bucket(len(eng.sched.running))] if graphs_ok else None
     sampler = ClockSampler(dev.index)
     dev_ms, e2e_ms, step_times, per_point = 0.0, 0.0, [], []
     with sampler:
@@ -282,13 +292,17 @@ def main():
             advance_context(eng, model, ctx_target, seed=ctx_target)
             seqs = [{"tokens": [r.all_tokens[r.cached]], "start": r.cached, "pages": r.pages}
                     for r in eng.sched.running]
-            eng.graphs.stage(gr, seqs)
+            if gr is not None:
+                eng.graphs.stage(gr, seqs)
             barrier()
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record()
             for _ in range(k):
-                gr.graph.replay()
+                if gr is not None:
+                    gr.graph.replay()
+                else:
+                    eng.step()            # eager library arm: its step is the whole engine step
             e1.record()
             barrier()
             d_ms = max_over_ranks(e0.elapsed_time(e1))
@@ -313,7 +327,7 @@ def main():
                               "p50_tpot_ms": round(statistics.median(pt) * 1e3, 3)})
     step_ms = dev_ms / args.steps
     trace_us = None
-    if args.trace and gr.trace_names:
+    if args.trace and gr is not None and gr.trace_names:
         tr = model.tracer
         gr.graph.replay()
         st = tr.stamps()
@@ -328,7 +342,7 @@ def main():
     h2d = local_batch * (4 + 4 + 8 + 4 + 16) + local_batch * eng.graphs.max_pages * 4
     d2h = local_batch * 8
     launches, graph_nodes = count_launches(gr) if args.impl == "native" else (None, None)
-    if os.environ.get("B200_BENCH_PROFILE") == "1":
+    if os.environ.get("B200_BENCH_PROFILE") == "1" and gr is not None:
         profile_breakdown(gr, ps.rank)
     clocks = sampler.summary()
     if ps.rank == 0:
@@ -363,7 +377,8 @@ def main():
                        "weight_format": weight_format(cfg, args.impl),
                        "switches": __import__("b200ds.utils.levers", fromlist=["switches"]).switches(),
                        "selfcheck": eng.selfcheck,
-                       "l2": "no flush: per-step weights+KV >> 126 MB L2", "init_s": round(t_init, 1)},
+                       "l2": "no flush: per-step weights+KV >> 126 MB L2", "init_s": round(t_init, 1),
+                       "decode": "cuda graph replay" if gr is not None else "eager engine steps (graph capture failed)"},
         }
         if trace_us is not None:
             out["trace_us_per_step"] = trace_us      # traced run: timing includes the stamp launches

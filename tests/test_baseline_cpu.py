@@ -61,3 +61,17 @@ def test_library_decode_attention_matches_reference():
                              pos, 0.07, ps)
     assert pages == bt.shape[1]
     assert ((got - want).norm() / want.norm()).item() < 2e-2
+
+
+def test_library_sampler_matches_reference():
+    g = torch.Generator().manual_seed(2)
+    T, V = 6, 300
+    logits = torch.randn(T, V, generator=g) * 3
+    temperature = torch.tensor([0.0, 0.7, 1.0, 1.3, 0.5, 0.9])
+    top_p = torch.tensor([1.0, 0.9, 0.5, 1.0, 0.95, 0.8])
+    top_k = torch.tensor([0, 0, 20, 5, 0, 50], dtype=torch.int32)
+    for trial in range(5):
+        uniform = torch.rand(T, generator=g)
+        got = baseline.sample_torch(logits, temperature, top_p, top_k, uniform)
+        want = ref.sample(logits, temperature, top_p, top_k, uniform)
+        assert torch.equal(got, want), (trial, got, want)
