@@ -40,24 +40,46 @@ FLUSH = None
 
 
 def timed(fn, iters: int) -> float:
-    """Median device time (s) of fn() over `iters` cold-L2 launches."""
+    """Median device time (s) of fn() over `iters` cold-L2 launches.  fn is
+    captured once in a CUDA graph and the graph is replayed between the
+    events, so the host work inside fn (allocations, argument marshalling)
+    does not show up as device idle time; an fn that cannot be captured is
+    timed by direct calls."""
     global FLUSH
     if FLUSH is None:
         FLUSH = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     for _ in range(3):
         fn()
+    torch.cuda.synchronize()
+    run = fn
+    try:
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(g, stream=side):
+                fn()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        GRAPHS.append(g)
+        run = g.replay
+    except Exception:
+        torch.cuda.synchronize()
     ts = []
     for _ in range(iters):
         FLUSH.zero_()
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record()
-        fn()
+        run()
         b.record()
         torch.cuda.synchronize()
         ts.append(a.elapsed_time(b) / 1e3)
     ts.sort()
     return ts[len(ts) // 2]
+
+
+GRAPHS = []
 
 
 def report(name, shape, t, nbytes=0, flops=0, flop_peak=None, note=""):
