@@ -523,6 +523,8 @@ __global__ void __launch_bounds__(kBThreads) hc_boundary_kernel(
       for (int r = 0; r < kBRows; ++r) acc[j][r] = 0.f;
     const int64_t K = (int64_t)kHC * D;
     const int ks = kHC * Dq;
+    // unrolled: the fn loads of several column steps are in flight together
+#pragma unroll 5
     for (int k = lane * 4; k < ks; k += 128) {
       const int c = k / Dq, d = k % Dq;            // Dq % 4 == 0: a float4 never straddles streams
       const float* f = fn + (int64_t)c * D + d0 + d;
@@ -1069,13 +1071,21 @@ int b200_hc_boundary(void* X, int T, int hc, int D, const void* y, int64_t ldy, 
   if (y && (!post_in || !comb_in)) return -1;
   // C CTAs per row group: columns per CTA a multiple of 32 (quant blocks on
   // one CTA, whole float4s per stream), the rows' fp32 copies in shared memory
+  // (16-CTA clusters, a non-portable size the B200 supports, halve each
+  // CTA's slice of fn and of the rows; 8 where the attribute is refused)
+  auto kern = hc_boundary_kernel;
+  const bool c16 =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
+  if (!c16) cudaGetLastError();
   int C = 0;
-  for (int c = 8; c >= 1; c >>= 1)
-    if (D % (32 * c) == 0 && size_t(kBRows) * kHC * (D / c) * sizeof(float) <= 160 * 1024) { C = c; break; }
+  for (int c = c16 ? 16 : 8; c >= 1; c >>= 1)
+    if (D % (32 * c) == 0 && D / c >= 256 && size_t(kBRows) * kHC * (D / c) * sizeof(float) <= 160 * 1024) {
+      C = c;
+      break;
+    }
   if (C == 0 || (reinterpret_cast<uintptr_t>(fn) & 15)) return -2;
   const int Dq = D / C;
   const size_t smem = size_t(kBRows) * kHC * Dq * sizeof(float);
-  auto kern = hc_boundary_kernel;
   if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(C, (T + kBRows - 1) / kBRows);
