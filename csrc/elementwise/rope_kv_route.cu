@@ -201,31 +201,50 @@ __global__ void moe_gather_kernel(const uint8_t* xq, const uint8_t* xsf, const i
   moe::moe_gather_pair(xq, xsf, i / K, r, Kd, dq, dsf);
 }
 
-__global__ void moe_combine_kernel(const __nv_bfloat16* y, const int* pair_row, int T, int K, int D, const void* add,
-                                   int add_f32, void* out, int out_f32) {
+// out[t] = sum_j y[pair_row[t, j]] (+ add[t]): one CTA per token, each
+// thread 8 columns at a time with 16-byte loads of all K rows in flight
+// (the row ids are read once, before the column loop).
+constexpr int kCombMaxK = 16;
+__global__ void __launch_bounds__(128) moe_combine_kernel(const __nv_bfloat16* y, const int* pair_row, int T, int K,
+                                                          int D, const void* add, int add_f32, void* out,
+                                                          int out_f32) {
   const int t = blockIdx.x;
   pdl_wait();
   pdl_launch_dependents();   // dependents wait for this grid before touching its outputs
-  for (int c = threadIdx.x * 2; c < D; c += blockDim.x * 2) {
-    float a0 = 0.f, a1 = 0.f;
-    for (int j = 0; j < K; ++j) {
-      const int r = pair_row[t * K + j];
-      if (r >= 0) {
-        const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(y + (int64_t)r * D + c));
-        a0 += v.x;
-        a1 += v.y;
+  int rows[kCombMaxK];
+#pragma unroll
+  for (int j = 0; j < kCombMaxK; ++j) rows[j] = j < K ? __ldcg(pair_row + (int64_t)t * K + j) : -1;
+  for (int v = threadIdx.x; v < D / 8; v += blockDim.x) {
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < kCombMaxK; ++j) {
+      if (rows[j] < 0) continue;
+      const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(y + (int64_t)rows[j] * D) + v);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h[i]);
+        acc[2 * i] += f.x;
+        acc[2 * i + 1] += f.y;
       }
     }
+    const int64_t o = (int64_t)t * D + v * 8;
     if (add) {
-      a0 += ld_any(add, (int64_t)t * D + c, add_f32);
-      a1 += ld_any(add, (int64_t)t * D + c + 1, add_f32);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] += ld_any(add, o + i, add_f32);
     }
     if (out_f32) {
-      reinterpret_cast<float*>(out)[(int64_t)t * D + c] = a0;
-      reinterpret_cast<float*>(out)[(int64_t)t * D + c + 1] = a1;
+      float* of = reinterpret_cast<float*>(out) + o;
+      *reinterpret_cast<float4*>(of) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      *reinterpret_cast<float4*>(of + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
     } else {
-      *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<__nv_bfloat16*>(out) + (int64_t)t * D + c) =
-          __floats2bfloat162_rn(a0, a1);
+      uint4 outv;
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&outv);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(out) + o) = outv;
     }
   }
 }
@@ -281,7 +300,8 @@ int b200_moe_gather(const uint8_t* xq, const uint8_t* xsf, const int* pair_row, 
 int b200_moe_combine(const void* y, const int* pair_row, int T, int K, int D, const void* add, int add_f32, void* out,
                      int out_f32, cudaStream_t st) {
   if (T <= 0) return 0;
-  b200::launch_pdl(moe_combine_kernel, dim3(T), dim3(256), 0, st, reinterpret_cast<const __nv_bfloat16*>(y), pair_row, T, K, D, add, add_f32,
-                                        out, out_f32);
+  if (K > kCombMaxK || D % 8) return -1;
+  b200::launch_pdl(moe_combine_kernel, dim3(T), dim3(128), 0, st, reinterpret_cast<const __nv_bfloat16*>(y), pair_row,
+                   T, K, D, add, add_f32, out, out_f32);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
