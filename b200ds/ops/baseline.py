@@ -173,17 +173,17 @@ def moe_experts_grouped(x: torch.Tensor, w: torch.Tensor, ids: torch.Tensor, ex,
     return out.to(out_dtype)
 
 
-_UNTILED = {}
-
-
 def _untiled(ex):
+    """Row-major copy of tiled expert weights, kept on the ExpertWeights
+    object (it lives and dies with the weights)."""
     from .quant import untile_rows128
     import dataclasses
-    key = id(ex)
-    if key not in _UNTILED:
-        u = lambda t: MXFP8Tensor(untile_rows128(t.data.view(torch.uint8)).view(t.data.dtype), t.sf, t.rows)
-        _UNTILED[key] = dataclasses.replace(ex, w13=u(ex.w13), w2=u(ex.w2), tiled=False)
-    return _UNTILED[key]
+    u = getattr(ex, "_untiled", None)
+    if u is None:
+        f = lambda t: MXFP8Tensor(untile_rows128(t.data.view(torch.uint8)).view(t.data.dtype), t.sf, t.rows)
+        u = dataclasses.replace(ex, w13=f(ex.w13), w2=f(ex.w2), tiled=False)
+        object.__setattr__(ex, "_untiled", u)
+    return u
 
 
 def grouped_mx_ok(dev) -> bool:
