@@ -85,6 +85,7 @@ class FusedAllReduce:
         x = a if (a.dtype == torch.bfloat16 and a.is_contiguous()) else a.to(torch.bfloat16).contiguous()
         y = torch.empty(T, H, dtype=torch.bfloat16, device=a.device) if (keep_bf16 or not quantize) else None
         qa = alloc_qact(T, H, a.device) if quantize else None
+        self._rows = T
         if self._one_kernel():
             self._fused(x, None, None, T, residual, w, eps, y, qa)
             return self._done(y, qa, residual)
@@ -98,9 +99,13 @@ class FusedAllReduce:
         whose rows are summed through the switch by one rank per CTA (switch
         `nvls_one_kernel`; otherwise NVLS keeps push + reduce kernels)."""
         from ..utils import levers
-        if self.nvls is None:
-            return levers.on("ar_one_kernel")
-        return levers.on("nvls_one_kernel")
+        if self.nvls is not None:
+            return levers.on("nvls_one_kernel")
+        # measured (benchmarks/collectives.py, one B200 box): one kernel wins
+        # while the pushed rows are few (2 ranks x 64 rows: 23.2 vs 25.8 us;
+        # 8 ranks x 1 row: 29.9 vs 38.6 us); at 8 ranks x 64 rows the push
+        # kernel's 296 CTAs store faster than one CTA per row (48.0 vs 55.7 us)
+        return levers.on("ar_one_kernel") and self.world * self._rows <= 256
 
     def _fused(self, x, pair_row, add, T, residual, w, eps, y, qa):
         from .. import _C
@@ -163,6 +168,7 @@ class FusedAllReduce:
         T = part.pair_row.shape[0]
         H = part.y.shape[1]
         add = part.add.to(torch.bfloat16).contiguous() if part.add is not None else None
+        self._rows = T
         if self._one_kernel():
             y, qa = self._outs(T, H, part.y.device, quantize)
             self._fused(part.y, part.pair_row, add, T, residual, ln_w, eps, y, qa)
@@ -235,7 +241,10 @@ class _Nvls:
         group, so all ranks take the same path); else None."""
         import os
         from ..utils import levers
-        want = levers.on("nvls") and world >= int(os.environ.get("B200_NVLS_MIN_WORLD", "4"))
+        # off at <= 8 ranks unless asked for: measured on 8 B200s at decode
+        # sizes the NVLS all-reduce (77 us at 64 rows) loses to the push
+        # protocol (48 us) and to NCCL (34 us), and NCCL wins large messages
+        want = levers.on("nvls") and world >= int(os.environ.get("B200_NVLS_MIN_WORLD", "16"))
         if not want:
             return None
         obj, ok = None, 0

@@ -122,7 +122,8 @@ register("fused_comm", "B200_FUSED_COMM", True,
          "device-initiated NVLink collectives fused into the producing / consuming kernels")
 register("nvls", "B200_NVLS", True,
          "tensor-parallel all-reduces through NVLink multicast (multimem.ld_reduce / multimem.st in the switch) on "
-         "groups of B200_NVLS_MIN_WORLD (default 4) or more ranks with multicast support")
+         "groups of B200_NVLS_MIN_WORLD or more ranks with multicast support (default 16: off on one 8-GPU "
+         "box, where it measured slower than the push protocol and NCCL)")
 register("l2_prefetch", "B200_L2_PREFETCH", True,
          "decode layers pull the o-projection (and shared-expert) weights into L2 on a low-priority side stream "
          "while attention runs")
