@@ -117,14 +117,17 @@ _GROUPED_MX_OK = None
 
 def _scaled_grouped(aq, asf, w, offs):
     """[R, K] MXFP8 rows (groups at offs, 128-row aligned) x expert weights
-    w [E, N, K] (MXFP8) -> [R, N] bf16."""
+    w [E, N, K] (MXFP8) -> [R, N] bf16.  The rows' scales go in as [R, K/32],
+    each expert's as one row of its blocked (32_4_4) scale bytes [E, N*K/32]:
+    the shapes PyTorch's 2d x 3d block-scaled grouped GEMM accepts (checked
+    on a B200: 1.7e-3 relative to the dequantized product)."""
     import torch.nn.functional as F
     R, K = aq.shape
     E, N = w.data.shape[0], w.data.shape[1]
     sw = F.SwizzleType.SWIZZLE_32_4_4
     return F.scaled_grouped_mm(aq.view(torch.float8_e4m3fn), w.data.view(torch.float8_e4m3fn).transpose(-2, -1),
                                asf.view(torch.float8_e8m0fnu).view(R, K // 32), F.ScalingType.BlockWise1x32,
-                               w.sf.view(torch.float8_e8m0fnu).view(E, N, K // 32), F.ScalingType.BlockWise1x32,
+                               w.sf.view(torch.float8_e8m0fnu).view(E, -1), F.ScalingType.BlockWise1x32,
                                swizzle_a=sw, swizzle_b=sw, offs=offs, output_dtype=torch.bfloat16)
 
 
