@@ -136,7 +136,7 @@ register("ar_one_kernel", "B200_AR_ONE_KERNEL", True,
 register("nvls_one_kernel", "B200_NVLS_ONE_KERNEL", False,
          "NVLS groups: one kernel per all-reduce - each CTA's rows stored locally, summed through the switch by "
          "rank c % world and broadcast back, per-CTA flags (off: push kernel + NVLS reduce kernel)")
-register("hc_boundary", "B200_HC_BOUNDARY", False,
+register("hc_boundary", "B200_HC_BOUNDARY", True,
          "V4 family, decode-sized batches: hc_post + the mHC mixes (fp32, CUDA cores) + coefficients + the next "
          "sublayer's normed input as one kernel, a thread-block cluster per row")
 register("deterministic", "B200_DETERMINISTIC", False,
