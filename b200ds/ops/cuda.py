@@ -579,8 +579,11 @@ def moe_experts_ep(h, w, ids, ex, T_step: int, n_experts_total: int, ep, far=Non
     bn1, bn2 = moe_tiles(exp_rows)
     max_rows = round_up(Tg * K, 128) + E * 128
     ids = (ids if ids.dtype == torch.int32 else ids.int()).contiguous()
+    # peer pull (fused expert kernel only): the rows stay in their source
+    # rank's region and the producer warps of the owners read them over NVLink
+    peer = _pulls(bn1, bn2) and levers.on("ep_peer_pull") and ep.world <= 8
     _C.ep_dispatch(q, sf, g, Hd, ids, w.float().contiguous(), T_step, n_experts_total // ep.world, ep.bases,
-                   ep.rank, ep.max_t, ep.epoch, ep.push_ticket)
+                   ep.rank, ep.max_t, ep.epoch, ep.push_ticket, peer_pull=peer)
     seg_start = torch.empty(E, dtype=torch.int32, device=dev)
     seg_count = torch.empty(E, dtype=torch.int32, device=dev)
     tt1 = torch.empty(E + 1, dtype=torch.int32, device=dev)
@@ -601,8 +604,14 @@ def moe_experts_ep(h, w, ids, ex, T_step: int, n_experts_total: int, ep, far=Non
     if pulls:
         # received rows read in place (row index = owner rank * T_step + t);
         # ep_align advanced the epoch, so they sit at parity (epoch + 1) & 1
-        pull = dict(row_token=row_token, src_q=[ep.recv_q], src_sf=[ep.recv_sf], src_g=[ep.recv_g] if fp4 else [],
-                    src_rows=ep.world * ep.max_t, src_epoch=ep.epoch, src_epoch_add=1, src_par_bytes=ep.par_bytes)
+        if peer:
+            # row g = source rank * T_step + t sits at row t of the source's region
+            pull = dict(row_token=row_token, src_q=ep.src_q, src_sf=ep.src_sf, src_g=ep.src_g if fp4 else [],
+                        src_rows=T_step, src_epoch=ep.epoch, src_epoch_add=1, src_par_bytes=ep.par_bytes)
+        else:
+            pull = dict(row_token=row_token, src_q=[ep.recv_q], src_sf=[ep.recv_sf],
+                        src_g=[ep.recv_g] if fp4 else [], src_rows=ep.world * ep.max_t, src_epoch=ep.epoch,
+                        src_epoch_add=1, src_par_bytes=ep.par_bytes)
         if comb:
             pull.update(c_row_pair=row_pair, c_K=K, c_T_step=T_step, c_bases=far.bases, c_rank=far.rank,
                         c_max_t=far.max_tokens, c_off=far.comb_off, c_epoch=far.epoch)

@@ -308,6 +308,11 @@ class EPDispatch:
         off, self.par_bytes, off_sf, off_g = (int(v) for v in _C.ep_region_layout(self.world, max_tokens, hidden, topk))
         mine = self.bases[self.rank] + off
         self.recv_q, self.recv_sf, self.recv_g = mine, mine + off_sf, mine + off_g
+        # every rank's region (peer pull: each rank's own rows stay there and
+        # the owners' expert kernels read them over NVLink)
+        self.src_q = [b + off for b in self.bases]
+        self.src_sf = [b + off + off_sf for b in self.bases]
+        self.src_g = [b + off + off_g for b in self.bases]
         torch.cuda.synchronize(dev)
         dist.barrier(group=group)
 

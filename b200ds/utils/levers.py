@@ -130,6 +130,10 @@ register("l2_prefetch", "B200_L2_PREFETCH", True,
 register("ep_combine_epilogue", "B200_EP_COMBINE_EPILOGUE", True,
          "expert parallelism: the experts' FC2 epilogue stores each weighted pair row straight into its token's "
          "owner rank (no separate combine kernel, no local round trip of the FC2 rows)")
+register("ep_peer_pull", "B200_EP_PEER_PULL", False,
+         "expert parallelism: routed rows stay on their source rank and the fused expert kernel's producer warps read "
+         "them over NVLink (only ids / weights are pushed); off: the dispatch stores each row into its owners' "
+         "regions")
 register("ar_one_kernel", "B200_AR_ONE_KERNEL", True,
          "push-mode all-reduces (and the TP MoE combine) run push + per-CTA arrivals + reduce + norm as one kernel "
          "instead of a push kernel and a reduce kernel")

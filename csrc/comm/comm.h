@@ -139,7 +139,8 @@ inline int64_t ep_buffer_bytes(int world, int max_t, int hidden, int K) {
 // fp4 = 1: q / sf / g are NVFP4 rows (hidden / 2 bytes, e4m3 per 16, global g).
 int b200_ep_dispatch(const uint8_t* q, const uint8_t* sf, const float* g, int fp4, const int* ids, const float* w,
                      int T_r, int T_step, int experts_per_rank, const EpPeers* peers, const uint32_t* epoch,
-                     uint32_t* ticket, cudaStream_t st);
+                     uint32_t* ticket, cudaStream_t st,
+                     int peer_pull = 0);
 // Routing layout over the received world * T_step tokens (waits for every
 // rank's dispatch; bounded).  release = 1 (no ep_gather follows: the expert
 // GEMM reads the received rows in place): also frees the parity (counters to

@@ -187,7 +187,8 @@ cudaStream_t cur() { return at::cuda::getCurrentCUDAStream().stream(); }
 
 void ep_dispatch(const at::Tensor& q, const at::Tensor& sf, c10::optional<at::Tensor> gs, int64_t hidden,
                  const at::Tensor& ids, const at::Tensor& w, int64_t T_step, int64_t experts_per_rank,
-                 std::vector<int64_t> bases, int64_t rank, int64_t max_t, const at::Tensor& epoch, at::Tensor ticket) {
+                 std::vector<int64_t> bases, int64_t rank, int64_t max_t, const at::Tensor& epoch, at::Tensor ticket,
+                 bool peer_pull) {
   TORCH_CHECK(q.is_cuda() && q.dim() == 2 && q.is_contiguous(), "q [T, hidden] e4m3 or [T, hidden/2] e2m1 pairs");
   TORCH_CHECK(ids.scalar_type() == at::kInt && ids.is_contiguous() && w.scalar_type() == at::kFloat && w.is_contiguous(),
               "ids int32 / w fp32 [T, K]");
@@ -200,7 +201,7 @@ void ep_dispatch(const at::Tensor& q, const at::Tensor& sf, c10::optional<at::Te
                                   ids.data_ptr<int>(),
                                   w.data_ptr<float>(), ids.size(0), T_step, experts_per_rank, &p,
                                   reinterpret_cast<const uint32_t*>(epoch.data_ptr()),
-                                  reinterpret_cast<uint32_t*>(ticket.data_ptr()), cur());
+                                  reinterpret_cast<uint32_t*>(ticket.data_ptr()), cur(), peer_pull ? 1 : 0);
   TORCH_CHECK(rc == 0, "ep_dispatch failed ", rc);
 }
 
@@ -317,7 +318,10 @@ void register_comm(pybind11::module& m) {
         pybind11::arg("ticket"), pybind11::arg("nctas"), pybind11::arg("mc") = 0);
   m.def("ep_buffer_size", &ep_buffer_size);
   m.def("ep_region_layout", &ep_region_layout);
-  m.def("ep_dispatch", &ep_dispatch);
+  m.def("ep_dispatch", &ep_dispatch, pybind11::arg("q"), pybind11::arg("sf"), pybind11::arg("gs"),
+        pybind11::arg("hidden"), pybind11::arg("ids"), pybind11::arg("w"), pybind11::arg("T_step"),
+        pybind11::arg("experts_per_rank"), pybind11::arg("bases"), pybind11::arg("rank"), pybind11::arg("max_t"),
+        pybind11::arg("epoch"), pybind11::arg("ticket"), pybind11::arg("peer_pull") = false);
   m.def("ep_align", &ep_align, pybind11::arg("bases"), pybind11::arg("rank"), pybind11::arg("max_t"),
         pybind11::arg("hidden"), pybind11::arg("K"), pybind11::arg("T_step"), pybind11::arg("first"), pybind11::arg("E"),
         pybind11::arg("seg_start"), pybind11::arg("seg_count"), pybind11::arg("row_token"), pybind11::arg("row_weight"),

@@ -51,7 +51,7 @@ __global__ void __launch_bounds__(kThreads) ep_dispatch_kernel(const uint8_t* __
                                                                 const int* __restrict__ ids,
                                                                 const float* __restrict__ w, int T_r, int T_step,
                                                                 int experts_per_rank, EpPeers P, const uint32_t* epoch,
-                                                                uint32_t* ticket) {
+                                                                uint32_t* ticket, int peer_pull) {
   __shared__ uint32_t mask_s;
   pdl_wait();
   if (threadIdx.x == 0) pdl_launch_dependents();
@@ -83,15 +83,20 @@ __global__ void __launch_bounds__(kThreads) ep_dispatch_kernel(const uint8_t* __
       did[(int64_t)row * K + k] = valid ? __ldcg(ids + t * K + k) : -1;
       dw[(int64_t)row * K + k] = valid ? __ldcg(w + t * K + k) : 0.f;
     }
-    if (!((mask >> d) & 1u)) continue;
+    // peer pull: the row stays in this rank's own region (row t), read there
+    // by the owners' expert kernels over NVLink; otherwise it is stored into
+    // every owner's region (row = rank * T_step + t)
+    const bool here = peer_pull ? (d == P.rank && mask != 0u) : ((mask >> d) & 1u) != 0u;
+    if (!here) continue;
+    const int drow = peer_pull ? t : row;
     const uint4* src = reinterpret_cast<const uint4*>(q + (int64_t)t * row_bytes);
-    uint4* dst = reinterpret_cast<uint4*>(reg + (int64_t)row * row_bytes);
+    uint4* dst = reinterpret_cast<uint4*>(reg + (int64_t)drow * row_bytes);
     for (int i = threadIdx.x; i < row_bytes / 16; i += kThreads) dst[i] = __ldcg(src + i);
-    if (fp4 && threadIdx.x == 0) reinterpret_cast<float*>(reg + P.off_g)[row] = __ldcg(g + t);
+    if (fp4 && threadIdx.x == 0) reinterpret_cast<float*>(reg + P.off_g)[drow] = __ldcg(g + t);
     uint8_t* dsf = reg + P.off_sf;
     for (int c = threadIdx.x; c < words; c += kThreads) {
       const uint32_t v = *reinterpret_cast<const uint32_t*>(sf + moe::sf_offset(t, 4 * c, kb));
-      *reinterpret_cast<uint32_t*>(dsf + moe::sf_offset(row, 4 * c, kb)) = v;
+      *reinterpret_cast<uint32_t*>(dsf + moe::sf_offset(drow, 4 * c, kb)) = v;
     }
   }
   comm::publish_push(P.base, P.world, P.rank, p, ticket);
@@ -226,12 +231,12 @@ __global__ void __launch_bounds__(256) ep_combine_rs_kernel(const __nv_bfloat16*
 
 int b200_ep_dispatch(const uint8_t* q, const uint8_t* sf, const float* g, int fp4, const int* ids, const float* w,
                      int T_r, int T_step, int experts_per_rank, const EpPeers* peers, const uint32_t* epoch,
-                     uint32_t* ticket, cudaStream_t st) {
+                     uint32_t* ticket, cudaStream_t st, int peer_pull) {
   if (T_step <= 0 || T_r > T_step || T_step > peers->max_t || peers->world > kArMaxRanks || peers->hidden % 128 ||
       experts_per_rank <= 0 || (fp4 && !g))
     return -1;
   b200::launch_pdl(b200::ep::ep_dispatch_kernel, dim3(T_step), dim3(b200::ep::kThreads), 0, st, q, sf, g, fp4, ids, w,
-                   T_r, T_step, experts_per_rank, *peers, epoch, ticket);
+                   T_r, T_step, experts_per_rank, *peers, epoch, ticket, peer_pull);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
 

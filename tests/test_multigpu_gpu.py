@@ -148,6 +148,10 @@ def _dp_rank(rank, world, comm_impl, fmt="mxfp8"):
     from b200ds.models.loader import build_model
     from b200ds.models.reference import init_weights
     from b200ds.parallel.state import ParallelState, init_parallel
+    from b200ds.utils import levers
+    if comm_impl == "peer":       # the expert kernels read the routed rows from their source ranks over NVLink
+        levers.set_switch("ep_peer_pull", True)
+        comm_impl = "fused"
     ps = init_parallel(backend="nccl", dp_attention=True, timeout_s=60)
     ops.set_impl("native")
     cfg = small_gpu_config(num_attention_heads=16, expert_format=fmt)
@@ -168,14 +172,16 @@ def _dp_rank(rank, world, comm_impl, fmt="mxfp8"):
     return rank, out, ref
 
 
-@pytest.mark.parametrize("comm_impl,fmt", [("nccl", "mxfp8"), ("fused", "mxfp8"), ("fused", "nvfp4")])
+@pytest.mark.parametrize("comm_impl,fmt", [("nccl", "mxfp8"), ("fused", "mxfp8"), ("fused", "nvfp4"),
+                                           ("peer", "mxfp8"), ("peer", "nvfp4")])
 def test_dp2_ep2_matches_single_gpu(comm_impl, fmt):
     """DP attention + EP MoE on 2 GPUs, ranks with different token counts:
     each rank's logits follow a 1-GPU run of its own batch (fp8 noise only).
     The fused path exercises ep_dispatch / ep_align, the expert kernel
     reading the received rows in place from the dispatch buffer (alternating
-    parities over the layers) and the combine + reduce-scatter into
-    ar_reduce_norm."""
+    parities over the layers) and the combine stored by the FC2 epilogue into
+    the owners' slots; "peer" leaves the rows on their source ranks and the
+    expert kernel reads them over NVLink."""
     _needs(2)
     res = run_ranks(_dp_rank, 2, comm_impl, fmt, timeout=600)
     for rank, out, ref in res:
