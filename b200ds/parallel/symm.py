@@ -85,15 +85,14 @@ class FusedAllReduce:
         x = a if (a.dtype == torch.bfloat16 and a.is_contiguous()) else a.to(torch.bfloat16).contiguous()
         y = torch.empty(T, H, dtype=torch.bfloat16, device=a.device) if (keep_bf16 or not quantize) else None
         qa = alloc_qact(T, H, a.device) if quantize else None
-        self._rows = T
-        if self._one_kernel():
+        if self._one_kernel(T):
             self._fused(x, None, None, T, residual, w, eps, y, qa)
             return self._done(y, qa, residual)
         bases, epoch, ticket, mc = self._push_target()
         _C.ar_push(x, bases, self.rank, self.max_tokens, epoch, ticket, self.push_ctas, mc=mc)
         return self._reduce(T, H, 1, residual, w, eps, y, qa)
 
-    def _one_kernel(self) -> bool:
+    def _one_kernel(self, rows: int) -> bool:
         """Push, per-CTA arrivals and reduce + norm in one launch: the push
         protocol (switch `ar_one_kernel`) or, on NVLS groups, the variant
         whose rows are summed through the switch by one rank per CTA (switch
@@ -105,7 +104,7 @@ class FusedAllReduce:
         # while the pushed rows are few (2 ranks x 64 rows: 23.2 vs 25.8 us;
         # 8 ranks x 1 row: 29.9 vs 38.6 us); at 8 ranks x 64 rows the push
         # kernel's 296 CTAs store faster than one CTA per row (48.0 vs 55.7 us)
-        return levers.on("ar_one_kernel") and self.world * self._rows <= 256
+        return levers.on("ar_one_kernel") and self.world * rows <= 256
 
     def _fused(self, x, pair_row, add, T, residual, w, eps, y, qa):
         from .. import _C
@@ -168,8 +167,7 @@ class FusedAllReduce:
         T = part.pair_row.shape[0]
         H = part.y.shape[1]
         add = part.add.to(torch.bfloat16).contiguous() if part.add is not None else None
-        self._rows = T
-        if self._one_kernel():
+        if self._one_kernel(T):
             y, qa = self._outs(T, H, part.y.device, quantize)
             self._fused(part.y, part.pair_row, add, T, residual, ln_w, eps, y, qa)
             return self._done(y, qa, residual)

@@ -13,19 +13,14 @@ def _far(world, nvls=None):
 
 
 def test_one_kernel_only_for_few_pushed_rows():
-    f = _far(2)
-    f._rows = 64
-    assert f._one_kernel()                  # 2 ranks x 64 rows: one kernel measured faster
+    assert _far(2)._one_kernel(64)          # 2 ranks x 64 rows: one kernel measured faster
     f = _far(8)
-    f._rows = 1
-    assert f._one_kernel()                  # 8 ranks x 1 row: one kernel
-    f._rows = 64
-    assert not f._one_kernel()              # 8 ranks x 64 rows: push + reduce kernels
+    assert f._one_kernel(1)                 # 8 ranks x 1 row: one kernel
+    assert not f._one_kernel(64)            # 8 ranks x 64 rows: push + reduce kernels
     before = levers.switches()["ar_one_kernel"]
     try:
         levers.set_switch("ar_one_kernel", False)
-        f._rows = 1
-        assert not f._one_kernel()
+        assert not f._one_kernel(1)
     finally:
         levers.set_switch("ar_one_kernel", before)
 
