@@ -104,15 +104,20 @@ class FusedAllReduce:
         # while the pushed rows are few (2 ranks x 64 rows: 23.2 vs 25.8 us;
         # 8 ranks x 1 row: 29.9 vs 38.6 us); at 8 ranks x 64 rows the push
         # kernel's 296 CTAs store faster than one CTA per row (48.0 vs 55.7 us)
-        return levers.on("ar_one_kernel") and self.world * rows <= 256
+        import os
+        limit = int(os.environ.get("B200_AR_ONE_KERNEL_ROWS", "256"))
+        return levers.on("ar_one_kernel") and self.world * rows <= limit
 
     def _fused(self, x, pair_row, add, T, residual, w, eps, y, qa):
         from .. import _C
         n = self.nvls
         bases, epoch, ticket, mc = (n.bases, n.epoch, n.ticket, n.mc) if n is not None else \
             (self.bases, self.epoch, self.ticket, 0)
+        import os
+        # push mode: CTAs per row owner that share the NVLink stores (B200_AR_CHUNKS, default 1)
+        chunks = 1 if n is not None else max(1, min(8, int(os.environ.get("B200_AR_CHUNKS", "1"))))
         _C.ar_fused_norm(x, pair_row, add, T, bases, self.rank, self.max_tokens, epoch, ticket, residual, w, eps, y,
-                         qa.q if qa else None, qa.sf if qa else None, self.err, mc=mc)
+                         qa.q if qa else None, qa.sf if qa else None, self.err, mc=mc, chunks=chunks)
 
     @staticmethod
     def _done(y, qa, residual):

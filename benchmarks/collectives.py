@@ -15,6 +15,8 @@ o_proj GEMM + all-reduce (bf16 partial [M, 7168], K = 16384 / N):
   * push_ar        our one-shot NVLink push + reduce (+residual +RMSNorm
                    +MXFP8) as one kernel (per-CTA arrivals);
   * push2_ar       the same as a push kernel + a reduce kernel;
+  * push1_c{1,4}_ar the one-kernel variant at any row count with 1 / 4 CTAs
+                   per row owner sharing the NVLink stores;
   * nvls1_ar       one-kernel NVLS variant (rows stored locally, summed
                    through the switch by one rank per CTA, broadcast back);
   * nvls_ar        the same through NVLink multicast (multimem.ld_reduce /
@@ -142,6 +144,14 @@ def ar_part(ps, Ms):
         levers.set_switch("ar_one_kernel", False)
         res["push2_ar_us"] = timed(lambda: far_push.allreduce_add_rmsnorm(part, resid, ln, 1e-6, True), iters)
         levers.set_switch("ar_one_kernel", True)
+        # one kernel whatever the row count, its stores spread over 1 / 4 CTAs per row owner
+        os.environ["B200_AR_ONE_KERNEL_ROWS"] = str(1 << 30)
+        for ch in (1, 4):
+            os.environ["B200_AR_CHUNKS"] = str(ch)
+            res[f"push1_c{ch}_ar_us"] = timed(lambda: far_push.allreduce_add_rmsnorm(part, resid, ln, 1e-6, True),
+                                              iters)
+        os.environ.pop("B200_AR_ONE_KERNEL_ROWS")
+        os.environ["B200_AR_CHUNKS"] = "1"
         if far_nvls is not None:
             res["nvls_ar_us"] = timed(lambda: far_nvls.allreduce_add_rmsnorm(part, resid, ln, 1e-6, True), iters)
             levers.set_switch("nvls_one_kernel", True)

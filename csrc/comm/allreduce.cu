@@ -268,17 +268,23 @@ template <bool COMBINE>
 __global__ void __launch_bounds__(kThreads) ar_fused_norm_kernel(
     const __nv_bfloat16* __restrict__ x, const int* __restrict__ pair_row, int K, const __nv_bfloat16* __restrict__ add,
     int T, int hidden, ArPeers peers, uint32_t* epoch, uint32_t* ticket, float* residual, const float* __restrict__ w,
-    float eps, __nv_bfloat16* y, uint8_t* q, uint8_t* sf, uint32_t* err) {
+    float eps, __nv_bfloat16* y, uint8_t* q, uint8_t* sf, uint32_t* err, int S) {
+  // S CTAs per row owner: CTA b pushes column chunk b % S of the rows of
+  // owner c = b / S; every chunk CTA raises the owner's flag, and the chunk-0
+  // CTA waits for world * S arrivals and reduces the whole rows.
   __shared__ float red[32];
   __shared__ int ok_s;
   pdl_wait();
   if (threadIdx.x == 0) pdl_launch_dependents();
   const int p = (*epoch) & 1;
-  const int G = gridDim.x, c = blockIdx.x;
+  const int c = blockIdx.x / S, chunk = blockIdx.x % S;
+  const int G = gridDim.x / S;
   uint8_t* mine = peers.base[peers.rank];
   const int units = hidden >> 3;
+  const int u_per = (units + S - 1) / S;
+  const int u0 = chunk * u_per, u1 = min(units, u0 + u_per);
   for (int t = c; t < T; t += G) {
-    for (int u = threadIdx.x; u < units; u += kThreads) {
+    for (int u = u0 + threadIdx.x; u < u1; u += kThreads) {
       uint4 outv;
       if constexpr (COMBINE) {
         float acc[8];
@@ -325,19 +331,21 @@ __global__ void __launch_bounds__(kThreads) ar_fused_norm_kernel(
       asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(cta_counters(peers.base[d], p) + c), "r"(1u)
                    : "memory");
     int ok = 1;
-    const uint32_t* cnt = cta_counters(mine, p) + c;
-    const uint64_t t0 = globaltimer_ns();
-    while (ld_acquire_sys(cnt) < (uint32_t)peers.world) {
-      if (globaltimer_ns() - t0 > kWaitBudgetNs) {
-        atomicExch(err, kErrPeerTimeout);
-        ok = 0;
-        break;
+    if (chunk == 0) {
+      const uint32_t* cnt = cta_counters(mine, p) + c;
+      const uint64_t t0 = globaltimer_ns();
+      while (ld_acquire_sys(cnt) < (uint32_t)(peers.world * S)) {
+        if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+          atomicExch(err, kErrPeerTimeout);
+          ok = 0;
+          break;
+        }
       }
     }
     ok_s = ok;
   }
   __syncthreads();
-  if (ok_s) {
+  if (ok_s && chunk == 0) {
     for (int t = c; t < T; t += G) {
       row_add_norm_quant(t, hidden, recv_slot(mine, p, 0, peers.world, peers.max_t, hidden),
                          (int64_t)peers.max_t * hidden, peers.world, hidden, nullptr, nullptr, residual, w, eps, y, q,
@@ -349,7 +357,7 @@ __global__ void __launch_bounds__(kThreads) ar_fused_norm_kernel(
   if (threadIdx.x == 0) {
     __threadfence();
     const uint32_t tk = atomicAdd(ticket, 1u);
-    if (tk == (uint32_t)G - 1) {
+    if (tk == gridDim.x - 1) {
       uint32_t* cnt = cta_counters(mine, p);
       for (int i = 0; i < G; ++i) atomicExch(cnt + i, 0u);
       *ticket = 0u;
@@ -760,12 +768,13 @@ int b200_ep_comb_reduce_norm(int T_r, int hidden, int K, const int* ids, const v
 
 int b200_ar_fused_norm(const void* x, const int* pair_row, int K, const void* add, int T, int hidden,
                        const ArPeers* peers, uint32_t* epoch, uint32_t* ticket, float* residual, const float* w,
-                       float eps, void* y, uint8_t* q, uint8_t* sf, uint32_t* err, cudaStream_t st) {
+                       float eps, void* y, uint8_t* q, uint8_t* sf, uint32_t* err, cudaStream_t st, int chunks) {
   if (T <= 0) return 0;
   if (T > peers->max_t || hidden % 32 || hidden > b200::comm::kThreads * 8 * b200::comm::kMaxIt ||
-      (pair_row && K <= 0))
+      (pair_row && K <= 0) || chunks < 1 || chunks > 8)
     return -1;
   const int G = std::min(T, std::min(148, kArMaxCtas));
+  const int S = peers->mc ? 1 : chunks;       // the NVLS variant keeps one CTA per row owner
   const auto* xb = reinterpret_cast<const __nv_bfloat16*>(x);
   const auto* ab = reinterpret_cast<const __nv_bfloat16*>(add);
   auto* yb = reinterpret_cast<__nv_bfloat16*>(y);
@@ -780,11 +789,11 @@ int b200_ar_fused_norm(const void* x, const int* pair_row, int K, const void* ad
     return cudaGetLastError() == cudaSuccess ? 0 : 1;
   }
   if (pair_row)
-    b200::launch_pdl(b200::comm::ar_fused_norm_kernel<true>, dim3(G), dim3(b200::comm::kThreads), 0, st, xb, pair_row,
-                     K, ab, T, hidden, *peers, epoch, ticket, residual, w, eps, yb, q, sf, err);
+    b200::launch_pdl(b200::comm::ar_fused_norm_kernel<true>, dim3(G * S), dim3(b200::comm::kThreads), 0, st, xb,
+                     pair_row, K, ab, T, hidden, *peers, epoch, ticket, residual, w, eps, yb, q, sf, err, S);
   else
-    b200::launch_pdl(b200::comm::ar_fused_norm_kernel<false>, dim3(G), dim3(b200::comm::kThreads), 0, st, xb,
+    b200::launch_pdl(b200::comm::ar_fused_norm_kernel<false>, dim3(G * S), dim3(b200::comm::kThreads), 0, st, xb,
                      (const int*)nullptr, 0, (const __nv_bfloat16*)nullptr, T, hidden, *peers, epoch, ticket, residual,
-                     w, eps, yb, q, sf, err);
+                     w, eps, yb, q, sf, err, S);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }

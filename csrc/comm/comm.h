@@ -64,10 +64,12 @@ int b200_ar_reduce_norm(int T, int hidden, const ArPeers* peers, uint32_t* epoch
 // buffer's multicast address) CTA c stores its rows only into this rank's
 // own input slot, rank c % world sums them through the switch
 // (multimem.ld_reduce) and broadcasts the sum (multimem.st), and every
-// rank's CTA c normalises the broadcast rows.
+// rank's CTA c normalises the broadcast rows.  Push mode with chunks > 1: each
+// row owner's columns are pushed by `chunks` CTAs and reduced by the first.
 int b200_ar_fused_norm(const void* x, const int* pair_row, int K, const void* add, int T, int hidden,
                        const ArPeers* peers, uint32_t* epoch, uint32_t* ticket, float* residual, const float* w,
-                       float eps, void* y, uint8_t* q, uint8_t* sf, uint32_t* err, cudaStream_t st);
+                       float eps, void* y, uint8_t* q, uint8_t* sf, uint32_t* err, cudaStream_t st,
+                       int chunks = 1);
 int b200_moe_combine_push(const void* y, const int* pair_row, int T, int K, int hidden, const void* add,
                           const ArPeers* peers, const uint32_t* epoch, uint32_t* ticket, int nctas, cudaStream_t st);
 // NVLS all-reduce + residual + RMSNorm (+ MXFP8): waits for every rank's

@@ -70,7 +70,8 @@ void moe_combine_push(const at::Tensor& y, const at::Tensor& pair_row, c10::opti
 void ar_fused_norm(const at::Tensor& x, c10::optional<at::Tensor> pair_row, c10::optional<at::Tensor> add, int64_t T,
                    std::vector<int64_t> bases, int64_t rank, int64_t max_t, at::Tensor epoch, at::Tensor ticket,
                    at::Tensor residual, const at::Tensor& w, double eps, c10::optional<at::Tensor> y,
-                   c10::optional<at::Tensor> q, c10::optional<at::Tensor> sf, at::Tensor err, int64_t mc) {
+                   c10::optional<at::Tensor> q, c10::optional<at::Tensor> sf, at::Tensor err, int64_t mc,
+                   int64_t chunks) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() == 2, "x bf16 rows");
   TORCH_CHECK(residual.scalar_type() == at::kFloat && residual.is_contiguous(), "residual fp32");
   const bool comb = pair_row.has_value() && pair_row->defined();
@@ -92,7 +93,7 @@ void ar_fused_norm(const at::Tensor& x, c10::optional<at::Tensor> pair_row, c10:
                                     reinterpret_cast<float*>(residual.data_ptr()),
                                     reinterpret_cast<const float*>(w.data_ptr()), eps, optr<void>(y), optr<uint8_t>(q),
                                     optr<uint8_t>(sf), reinterpret_cast<uint32_t*>(err.data_ptr()),
-                                    at::cuda::getCurrentCUDAStream().stream());
+                                    at::cuda::getCurrentCUDAStream().stream(), int(chunks));
   TORCH_CHECK(rc == 0, "ar_fused_norm failed ", rc);
 }
 
@@ -305,7 +306,7 @@ void register_comm(pybind11::module& m) {
         pybind11::arg("T"), pybind11::arg("bases"), pybind11::arg("rank"), pybind11::arg("max_t"),
         pybind11::arg("epoch"), pybind11::arg("ticket"), pybind11::arg("residual"), pybind11::arg("w"),
         pybind11::arg("eps"), pybind11::arg("y"), pybind11::arg("q"), pybind11::arg("sf"), pybind11::arg("err"),
-        pybind11::arg("mc") = 0);
+        pybind11::arg("mc") = 0, pybind11::arg("chunks") = 1);
   m.def("ar_buffer_size", &ar_buffer_size);
   m.def("nvls_buffer_size", &nvls_buffer_size);
   m.def("nvls_ar_norm", &nvls_ar_norm);

@@ -34,6 +34,9 @@ def _rank(rank, world, comm_impl, kind):
     if nvls:      # the NVLS all-reduce (multicast) already at 2 ranks
         os.environ["B200_NVLS_MIN_WORLD"] = "2"
         comm_impl = "fused"
+    if comm_impl == "fused4":     # one-kernel all-reduce, 4 CTAs per row owner sharing the stores
+        os.environ["B200_AR_CHUNKS"] = "4"
+        comm_impl = "fused"
     ps = init_parallel(backend="nccl", timeout_s=60)
     ops.set_impl("native")
     # 32 heads: 16 per rank keeps both runs on the same tcgen05 MLA kernel
@@ -105,7 +108,7 @@ def _has_multicast():
         return False
 
 
-@pytest.mark.parametrize("comm_impl", ["nccl", "fused", "nvls"])
+@pytest.mark.parametrize("comm_impl", ["nccl", "fused", "fused4", "nvls"])
 @pytest.mark.parametrize("kind,tol", [("dense", 2e-2), ("moe", 1e-1)])
 def test_tp2_ep2_matches_single_gpu(comm_impl, kind, tol):
     """TP2/EP2 vs one GPU.  The runs differ only in how partial sums are
