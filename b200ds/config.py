@@ -353,6 +353,8 @@ class EngineConfig:
     max_prefill_tokens: int = 16384  # chunked-prefill budget per step
     schedule_policy: str = "fcfs"    # admission order: "fcfs", "lpm" (longest cached prefix first), "priority"
     mixed_steps: bool = False        # prefill steps also advance running requests by one decode token
+    context_parallel: bool = False   # DP attention: long prompts prefill on every rank (rows split round-robin)
+    cp_min_tokens: int = 8192        # server: prompts at least this long take the context-parallel path
     prefill_tail: bool = True        # window-only late layers (V4 family) run only on each prompt's tail rows
     kv_cache_fraction: float = 0.85  # of free HBM after weights
     max_kv_pages: Optional[int] = None

@@ -19,8 +19,9 @@ model_node.py:480-482 and the logits processor lgp.py:555).
 from __future__ import annotations
 
 import time
+from collections import deque
 from dataclasses import dataclass, field
-from typing import Dict, List, Optional, Sequence, Union
+from typing import Deque, Dict, List, Optional, Sequence, Union
 
 import torch
 
@@ -122,6 +123,15 @@ class Engine:
         # each step on the mode and on the per-rank token rows of the MoE
         # exchange (gloo, host only), and an idle rank joins with a dummy.
         self.dp = bool(ecfg.dp_attention) and self.ps.ep_size > 1
+        # context-parallel prefill: every rank holds the same queue of long
+        # prompts (added on all ranks in the same order) and prefills its
+        # head together, chunk by chunk, ahead of the ranks' own steps
+        if ecfg.context_parallel and not self.dp:
+            raise ValueError("context_parallel needs dp_attention over more than one rank")
+        self.cp = bool(ecfg.context_parallel)
+        self._cp_wait: Deque[Request] = deque()
+        self._cp_cur: Optional[Request] = None
+        self._cp_seq = 0
         import os
         if ecfg.trace or os.environ.get("B200_TRACE", "0") == "1":
             from ..utils.trace import Tracer
@@ -143,15 +153,28 @@ class Engine:
         return max(16, int(free * self.ecfg.kv_cache_fraction) // per_page)
 
     # ------------------------------------------------------------------
-    def add_request(self, prompt: Union[str, Sequence[int]], params: Optional[SamplingParams] = None) -> Request:
+    def add_request(self, prompt: Union[str, Sequence[int]], params: Optional[SamplingParams] = None,
+                    cp_owner: Optional[int] = None) -> Request:
+        """Queue a request.  cp_owner (context_parallel engines): prefill the
+        prompt on every rank and decode it on rank cp_owner; every rank must
+        add it, in the same order relative to its other context-parallel
+        requests.  On the other ranks the returned request finishes after the
+        prefill with finish_reason "context_parallel_peer" and no tokens."""
         if isinstance(prompt, str):
             assert self.tokenizer is not None, "text prompts need a tokenizer"
             prompt = self.tokenizer.encode(prompt)
         params = params or SamplingParams()
         prompt = [int(t) for t in prompt]      # python ints (tensor / numpy rows accepted)
         self.check_request(prompt, params)
+        if cp_owner is not None:
+            self._cp_check(params, int(cp_owner))
         r = Request(self._next_rid, prompt, params)
         self._next_rid += 1
+        if cp_owner is not None:
+            r.cp_owner, r.cp_seq = int(cp_owner), self._cp_seq
+            self._cp_seq += 1
+            self._cp_wait.append(r)
+            return r
         self.sched.add(r)
         return r
 
@@ -192,6 +215,9 @@ class Engine:
         are freed, finish_reason becomes "abort".  Call between steps; SPMD
         ranks must abort the same requests in the same order."""
         if r.finished:
+            return
+        if r.cp_seq >= 0 and (r is self._cp_cur or r in self._cp_wait):
+            r.cp_abort = True          # dropped on every rank at the next agreed step
             return
         self.sched.abort(r)
         r.finished, r.finish_reason = True, "abort"
@@ -399,6 +425,9 @@ class Engine:
 
     def step(self) -> List[Request]:
         """Run one scheduler step; returns requests that finished."""
+        if self.cp and self._cp_agree():
+            self._step_lp = {}
+            return self._cp_step()
         st = self.sched.next_step()
         multi = None
         self._step_lp: Dict[int, list] = {}
@@ -424,7 +453,6 @@ class Engine:
                 r.cached += len(new)
         self._check_device_errors()
         now = time.perf_counter()
-        done = []
         self.stats["steps"] += 1
         if st.kind == "prefill":
             n_pre = len(st.chunks) - st.decode_rows
@@ -432,6 +460,12 @@ class Engine:
             self.stats["decode_tokens"] += st.decode_rows
         else:
             self.stats["decode_tokens"] += sum(len(m) for m in multi)
+        return self._emit(st, multi, now)
+
+    def _emit(self, st: Step, multi, now: float) -> List[Request]:
+        """Append each sampled request's new tokens, apply the stop rules and
+        release finished requests; returns those."""
+        done = []
         for r, smp, new in zip(st.reqs, st.sample, multi):
             if not smp:
                 continue
@@ -744,7 +778,7 @@ class Engine:
         return {"running": len(sc.running), "prefilling": len(sc.prefilling), "waiting": len(sc.waiting),
                 "kv_pages_total": self.pool.num_pages, "kv_pages_free": self.pool.num_free,
                 "admitted_prompt_tokens": sc.admitted_prompt_tokens, "prefix_hit_tokens": sc.prefix_hit_tokens,
-                "preemptions": sc.preemptions,
+                "preemptions": sc.preemptions, "cp_queue": len(self._cp_wait) + (self._cp_cur is not None),
                 "host_offloads": self.radix.offloads if self.radix is not None else 0,
                 "host_restores": self.radix.restores if self.radix is not None else 0}
 
@@ -792,8 +826,122 @@ class Engine:
     def _drain_dp(self) -> None:
         if self.dp:
             # keep stepping (as an idle rank) until every rank is done
-            while self._dp_forward(None) is not None:
-                pass
+            while True:
+                if self.cp and self._cp_agree():
+                    self._cp_step()
+                    continue
+                if self._dp_forward(None) is None:
+                    break
+
+    # ------------------------------------------------------------------
+    # Context-parallel prefill (DP attention): one long prompt on all ranks
+    def _cp_check(self, params: SamplingParams, owner: int) -> None:
+        if not self.cp:
+            raise ValueError("context-parallel requests need EngineConfig(context_parallel=True)")
+        if not getattr(self.model, "supports_cp", False):
+            raise ValueError("this model family has no context-parallel prefill")
+        if self.mtp is not None:
+            raise ValueError("context-parallel prefill runs without the MTP draft module")
+        if params.prompt_logprobs is not None:
+            raise ValueError("context-parallel requests do not return prompt log-probabilities")
+        if not 0 <= owner < self.ps.ep_size:
+            raise ValueError(f"cp_owner {owner} is not a rank of the {self.ps.ep_size}-rank group")
+
+    def _cp_all(self) -> List[Request]:
+        return ([self._cp_cur] if self._cp_cur is not None else []) + list(self._cp_wait)
+
+    def _cp_drop(self, seq: int) -> None:
+        """Drop the context-parallel request `seq` (an agreed abort)."""
+        for r in self._cp_all():
+            if r.cp_seq == seq:
+                if r is self._cp_cur:
+                    self._cp_cur = None
+                else:
+                    self._cp_wait.remove(r)
+                if r.pages:
+                    self.pool.release(r.pages)
+                    r.pages = []
+                r.finished, r.finish_reason, r.t_done = True, "abort", time.perf_counter()
+                return
+
+    def _cp_agree(self) -> bool:
+        """Host agreement before each step: do all ranks hold the same
+        context-parallel queue, does the head's prompt fit every rank's pool,
+        is an abort pending.  True: this step prefills the head's next chunk."""
+        import torch.distributed as dist
+        from ..kv.pool import OutOfPages
+        head = self._cp_cur or (self._cp_wait[0] if self._cp_wait else None)
+        fail = 0
+        if head is not None and not head.pages:
+            need = self.pool.pages_for(len(head.prompt))
+            if self.pool.num_free < need and self.radix is not None:
+                self.radix.evict(need - self.pool.num_free)
+            if self.pool.num_free < need:
+                fail = 1
+            else:
+                head.pages = self.pool.alloc(need)
+        n = len(self._cp_wait) + (self._cp_cur is not None)
+        ab = max([r.cp_seq + 1 for r in self._cp_all() if r.cp_abort], default=0)
+        v = torch.tensor([n, -n, fail, ab, int(self.sched.has_work)], dtype=torch.int64)
+        dist.all_reduce(v, op=dist.ReduceOp.MAX, group=self.ps.cpu_group)
+        n_max, n_min, any_fail, ab, busy = int(v[0]), -int(v[1]), int(v[2]), int(v[3]), int(v[4])
+        if n_max != n_min:
+            raise RuntimeError(f"ranks disagree on the context-parallel queue ({n_min} .. {n_max} requests): "
+                               "every rank must add each context-parallel request")
+        if ab:
+            self._cp_drop(ab - 1)
+            return False
+        if n_max == 0:
+            return False
+        if any_fail:
+            if head is not None and head is not self._cp_cur and head.pages:
+                self.pool.release(head.pages)      # let this rank's running requests use them meanwhile
+                head.pages = []
+            if not busy:
+                raise OutOfPages("a context-parallel prompt does not fit in some rank's KV pool")
+            return False
+        if self._cp_cur is None:
+            self._cp_cur = self._cp_wait.popleft()
+        return True
+
+    def _cp_step(self) -> List[Request]:
+        """Prefill the next chunk of the context-parallel head on every rank
+        (this rank's rows: positions start + rank + k * W); after the last
+        chunk the owner samples the first token and the request joins its
+        running set, the other ranks release their copy of the cache."""
+        from ..parallel.cp import build_cp_batch, holder_of_last
+        r = self._cp_cur
+        W, me = self.ps.ep_size, self.ps.ep_rank
+        start = r.cached
+        n = min(len(r.prompt) - start, self.ecfg.max_prefill_tokens * W)
+        fb = build_cp_batch(r.prompt, start, n, W, me, r.pages, self.ecfg.page_size)
+        own = fb.cp.counts[me]
+        m = self.model
+        fb = self._to_device(fb)
+        h = m._hidden(fb)
+        r.cached = start + n
+        self.stats["steps"] += 1
+        self.stats["prefill_tokens"] += own
+        final = r.cached >= len(r.prompt)
+        row = m._last_hidden(h, fb) if final else None
+        self._check_device_errors()
+        if not final:
+            return []
+        # the prompt's last row: broadcast from the rank that computed it
+        row = self.ps.ep_all_gather(row.contiguous())[holder_of_last(n, W)].unsqueeze(0)
+        self._cp_cur = None
+        now = time.perf_counter()
+        if me == r.cp_owner:
+            logits = ops.lm_head_logits(row, m.lm_head, self.ps)
+            st = Step("prefill", [r], [r.prompt[start:start + n]], [start], [True])
+            toks = self._sample(st, logits)
+            self._note_lp(st.reqs, logits, range(1), [toks[:1]], st.sample)
+            self.sched.running.append(r)
+            return self._emit(st, [toks[:1]], now)
+        # a peer: its cache of the prompt goes to the prefix cache (or is freed)
+        self.sched.release(r, cache_prefix=True)
+        r.finished, r.finish_reason, r.t_done = True, "context_parallel_peer", now
+        return [r]
 
     def _output(self, r: Request) -> GenerateOutput:
         n = len(r.output)

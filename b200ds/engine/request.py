@@ -54,6 +54,12 @@ class Request:
     # per prompt position (prompt_logprobs set): None for the first token, then (token, logprob, top-n)
     prompt_lp: List[Optional[tuple]] = field(default_factory=list)
     gen: Optional[torch.Generator] = None
+    # context-parallel prefill (DP attention): the rank that decodes the
+    # request (None = an ordinary request), its place in the ranks' shared
+    # context-parallel queue, and an abort waiting for the ranks to agree
+    cp_owner: Optional[int] = None
+    cp_seq: int = -1
+    cp_abort: bool = False
 
     @property
     def all_tokens(self) -> List[int]:

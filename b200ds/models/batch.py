@@ -35,6 +35,9 @@ class ForwardBatch:
     # Prefill tail [B]: window-only late layers compute only the rows at
     # positions >= tail_from[sequence] (and each sequence's last row)
     tail_from: Optional[torch.Tensor] = None
+    # Context-parallel prefill chunk (parallel.cp.CPLayout): the layer stack
+    # all-gathers each layer's new cache rows over the ranks before attention
+    cp: Optional[object] = None
 
     @property
     def num_tokens(self) -> int:

@@ -96,6 +96,8 @@ class LayerWeights:
 
 
 class DeepseekModel:
+    supports_cp = True        # context-parallel prefill under DP attention (parallel/cp.py)
+
     def __init__(self, cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState,
                  layers: List[LayerWeights], embed: torch.Tensor, final_ln: torch.Tensor,
                  lm_head: torch.Tensor, device, kv_dtype=torch.float8_e4m3fn):
@@ -183,6 +185,8 @@ class DeepseekModel:
                                 keep_hf=bool(c.index_n_heads))
         ops.kv_store(qkv[:, ql:ql + c.kv_cache_dim], aw.kv_a_ln, c.rms_norm_eps, self.rope_table, fb.positions,
                      self.kv_cache[i], fb.out_slots, self.kv_scale[i], c.kv_lora_rank)
+        if fb.cp is not None and not c.index_n_heads:
+            self._cp_gather(i, fb)
         qo = aw.q_b(q_lat, out_dtype=torch.float32 if self.device.type == "cpu" else torch.bfloat16)
         q = qo[:, : self.heads * c.qk_head_dim].view(T, self.heads, c.qk_head_dim)
         topk = None
@@ -213,8 +217,20 @@ class DeepseekModel:
         q_raw = qo[:, self.heads * c.qk_head_dim: self.heads * c.qk_head_dim + nh * hd]
         ops.index_k_store(k_raw, aw.ix_k_norm_w, aw.ix_k_norm_b, 1e-6, self.rope_table, fb.positions,
                           self.ix_cache[i], self.ix_scale[i], fb.out_slots)
+        if fb.cp is not None:
+            self._cp_gather(i, fb)
         return ops.indexer_topk(q_raw, w_raw, (nh * hd) ** -0.5, self.rope_table, self.ix_cache[i],
                                 self.ix_scale[i], fb, self.page_size, c.index_topk, c.index_swa)
+
+    def _cp_gather(self, i: int, fb: ForwardBatch) -> None:
+        """Context-parallel chunk: every rank's new cache rows of layer i
+        (latent + rope, and the indexer key + scale of sparse models) into
+        this rank's cache before any query of the chunk attends."""
+        from ..parallel.cp import gather_rows
+        bufs = [self.kv_cache[i]]
+        if self.cfg.index_n_heads:
+            bufs += [self.ix_cache[i], self.ix_scale[i]]
+        gather_rows(bufs, fb, self.ps)
 
     def _ffn(self, i: int, lw: LayerWeights, h, fb: ForwardBatch) -> torch.Tensor:
         c = self.cfg

@@ -326,13 +326,19 @@ class _Refused:
 
 
 def _dp_admit(eng, ps, batch, own) -> None:
+    """Queue this rank's share of a broadcast batch.  With context
+    parallelism on, prompts of at least cp_min_tokens are queued on every
+    rank (all ranks prefill them; the assigned rank decodes and streams)."""
     for prompt, spd, owner, gid in batch:
-        if owner == ps.rank:
+        cp = getattr(eng, "cp", False) and len(prompt) >= eng.ecfg.cp_min_tokens
+        if owner == ps.rank or cp:
             sp = SamplingParams(**spd)
             try:
-                own[gid] = [eng.add_request(prompt, sp), 0]
+                r = eng.add_request(prompt, sp, cp_owner=owner) if cp else eng.add_request(prompt, sp)
             except ValueError as e:
-                own[gid] = [_Refused(sp, str(e)), 0]
+                r = _Refused(sp, str(e))
+            if owner == ps.rank:
+                own[gid] = [r, 0]
 
 
 def _dp_updates(own) -> list:
@@ -1022,6 +1028,9 @@ def main(argv=None):
     ap.add_argument("--spec-k", type=int, default=4, help="draft tokens verified per step")
     ap.add_argument("--trace", action="store_true", help="device timestamps per layer phase")
     ap.add_argument("--mixed-steps", action="store_true", help="decode tokens ride along with prefill chunks")
+    ap.add_argument("--context-parallel", action="store_true",
+                    help="with --dp-attention: long prompts prefill on every rank")
+    ap.add_argument("--cp-min-tokens", type=int, default=8192, help="shortest prompt that prefills context-parallel")
     ap.add_argument("--extend-graphs", action="store_true", help="replay prefill chunks from CUDA graphs")
     ap.add_argument("--page-size", type=int, default=64, help="tokens per KV page")
     ap.add_argument("--max-prefill-tokens", type=int, default=16384, help="chunked-prefill budget per step")
@@ -1058,7 +1067,8 @@ def main(argv=None):
                         max_prefill_tokens=args.max_prefill_tokens, kv_cache_fraction=args.kv_cache_fraction,
                         graph_batch_sizes=tuple(int(x) for x in args.graph_batch_sizes.split(",") if x),
                         prefill_tail=not args.no_prefill_tail, comm_impl=args.comm,
-                        schedule_policy=args.schedule_policy, host_kv_pages=args.host_kv_pages)
+                        schedule_policy=args.schedule_policy, host_kv_pages=args.host_kv_pages,
+                        context_parallel=args.context_parallel, cp_min_tokens=args.cp_min_tokens)
     eng = load_engine(args.model, weights=args.weights, ecfg=ecfg)
     tok = load_tokenizer(args.model)
     eng.tokenizer = tok

@@ -1,0 +1,136 @@
+"""Context-parallel prefill under DP attention on CPU (gloo): a long prompt
+prefills on every rank (rows split round-robin, each layer's new cache rows
+all-gathered), the owner rank decodes it, and its tokens must equal a
+single-process run of the same prompt; the ranks' own requests keep stepping
+in lockstep around the context-parallel chunks."""
+import dataclasses
+
+import pytest
+import torch
+
+from mp_util import run_ranks
+
+
+def _cfg(sparse: bool):
+    from b200ds.config import tiny_config
+    cfg = tiny_config()
+    if sparse:      # top-8 of up to 45 cached tokens: the gathered indexer keys matter
+        cfg = dataclasses.replace(cfg, index_n_heads=4, index_head_dim=32, index_topk=8)
+    return cfg
+
+
+def _prompts(cfg):
+    g = torch.Generator().manual_seed(11)
+    # the context-parallel prompt (33 tokens: chunks of 16, 16 and 1 at two
+    # ranks, so the last chunk leaves one rank without rows) and one ordinary
+    # request per rank
+    lens = [33, 12, 9]
+    return [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in lens]
+
+
+MAXT = [8, 6, 5]
+
+
+def _single(cfg, prompts, maxt):
+    from b200ds import build_model_from
+    from b200ds.config import EngineConfig
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.reference import init_weights
+    ecfg = EngineConfig(page_size=8, cuda_graphs=False)
+    eng = Engine(build_model_from(cfg, ecfg, init_weights(cfg, 0), device="cpu"), ecfg)
+    outs = eng.generate(prompts, [SamplingParams(max_tokens=n) for n in maxt])
+    return [o.token_ids for o in outs]
+
+
+def _rank(rank, world, sparse, owner):
+    from b200ds import build_model_from
+    from b200ds.config import EngineConfig
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.reference import init_weights
+    from b200ds.parallel.state import init_parallel
+    ps = init_parallel(backend="gloo", dp_attention=True)
+    cfg = _cfg(sparse)
+    ecfg = EngineConfig(page_size=8, cuda_graphs=False, tp_size=1, ep_size=world, dp_attention=True,
+                        context_parallel=True, max_prefill_tokens=8)
+    eng = Engine(build_model_from(cfg, ecfg, init_weights(cfg, 0), device="cpu", ps=ps), ecfg)
+    prompts = _prompts(cfg)
+    own = eng.add_request(prompts[1 + rank], SamplingParams(max_tokens=MAXT[1 + rank]))
+    cp = eng.add_request(prompts[0], SamplingParams(max_tokens=MAXT[0]), cp_owner=owner)
+    while not (own.finished and cp.finished):
+        eng.step()
+    eng._drain_dp()
+    return rank, own.output, cp.output, cp.finish_reason, eng.pool.num_free, eng.stats["prefill_tokens"]
+
+
+@pytest.mark.parametrize("sparse", [False, True])
+def test_cp2_prefill_matches_single(sparse):
+    cfg = _cfg(sparse)
+    prompts = _prompts(cfg)
+    ref = _single(cfg, prompts, MAXT)
+    owner = 1       # the prompt's last row is computed on rank 0: the row crosses ranks
+    res = run_ranks(_rank, 2, sparse, owner)
+    for rank, own, cp, reason, _, _ in res:
+        assert own == ref[1 + rank]
+        if rank == owner:
+            assert cp == ref[0]
+            assert reason == "length"
+        else:
+            assert cp == [] and reason == "context_parallel_peer"
+    # each rank prefilled its own prompt plus its half of the long one
+    # (33 = 8 + 8 + 1 rows on rank 0, 8 + 8 on rank 1)
+    assert {r[0]: r[5] for r in res} == {0: len(prompts[1]) + 17, 1: len(prompts[2]) + 16}
+
+
+def _rank_abort(rank, world):
+    from b200ds import build_model_from
+    from b200ds.config import EngineConfig
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.reference import init_weights
+    from b200ds.parallel.state import init_parallel
+    ps = init_parallel(backend="gloo", dp_attention=True)
+    cfg = _cfg(False)
+    ecfg = EngineConfig(page_size=8, cuda_graphs=False, tp_size=1, ep_size=world, dp_attention=True,
+                        context_parallel=True, max_prefill_tokens=8, enable_prefix_cache=False)
+    eng = Engine(build_model_from(cfg, ecfg, init_weights(cfg, 0), device="cpu", ps=ps), ecfg)
+    free0 = eng.pool.num_free
+    prompts = _prompts(cfg)
+    a = eng.add_request(prompts[0], SamplingParams(max_tokens=4), cp_owner=0)
+    b = eng.add_request(prompts[0][:20], SamplingParams(max_tokens=3), cp_owner=1)
+    eng.step()                      # first chunk of a
+    if rank == 0:
+        eng.abort(a)                # only the owner learns of the abort; the ranks agree on it
+    while not b.finished:
+        eng.step()
+    eng._drain_dp()
+    return rank, a.finish_reason, b.output, b.finish_reason, eng.pool.num_free == free0
+
+
+def test_cp2_abort_is_agreed():
+    cfg = _cfg(False)
+    ref = _single(cfg, [_prompts(cfg)[0][:20]], [3])
+    res = run_ranks(_rank_abort, 2)
+    for rank, ra, bout, rb, pages_back in res:
+        assert ra == "abort"
+        assert pages_back
+        if rank == 1:
+            assert bout == ref[0] and rb == "length"
+        else:
+            assert bout == [] and rb == "context_parallel_peer"
+
+
+def test_cp_layout_round_robin():
+    from b200ds.parallel.cp import build_cp_batch, holder_of_last, layout
+    pages = [5, 2, 9, 7]
+    lay = layout(3, 10, 3, pages, 4)            # positions 3..12 over 3 ranks
+    assert lay.counts == [4, 3, 3] and lay.tmax == 4
+    # chunk order: position 3 is rank 0 row 0, 4 is rank 1 row 0, ...
+    assert lay.src_rows.tolist() == [0, 4, 8, 1, 5, 9, 2, 6, 10, 3]
+    assert lay.dst_slots.tolist() == [pages[p // 4] * 4 + p % 4 for p in range(3, 13)]
+    fb = build_cp_batch(list(range(100, 120)), 3, 10, 3, 2, pages, 4)
+    assert fb.positions.tolist() == [5, 8, 11] and fb.input_ids.tolist() == [105, 108, 111]
+    assert holder_of_last(10, 3) == 0
+    empty = build_cp_batch(list(range(20)), 0, 1, 2, 1, pages, 4)     # rank 1 has no rows
+    assert empty.out_slots.tolist() == [0] and empty.cp.counts == [1, 0]

@@ -239,3 +239,65 @@ def test_v4_tp2_fused_boundary_matches_oracle():
         want.append(oracle.forward(seq.view(1, -1), 0, decode=False)[0, -1])
     want = torch.stack(want)
     assert _rel(res[0], want) < 0.15, _rel(res[0], want)
+
+
+def _cp_rank(rank, world):
+    import torch
+    import torch.distributed as dist
+    from b200ds import ops
+    from b200ds.config import EngineConfig, small_gpu_config
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.loader import build_model
+    from b200ds.models.reference import init_weights
+    from b200ds.parallel.state import ParallelState, init_parallel
+    ps = init_parallel(backend="nccl", dp_attention=True, timeout_s=60)
+    ops.set_impl("native")
+    cfg = small_gpu_config(num_attention_heads=16)
+    sd = init_weights(cfg, 0)
+    g = torch.Generator().manual_seed(21)
+    prompt = torch.randint(0, cfg.vocab_size, (300,), generator=g).tolist()
+
+    def first_logits(eng, **kw):
+        seen = []
+        orig = eng._sample
+        eng._sample = lambda st, lg: seen.append(lg.float().cpu()) or orig(st, lg)
+        r = eng.add_request(prompt, SamplingParams(max_tokens=2), **kw)
+        while not r.finished:
+            eng.step()
+        return r, (seen[0] if seen else None)
+
+    # chunks of 256 rows (128 a rank: the fused expert-parallel exchange) and 44
+    ecfg = EngineConfig(tp_size=1, ep_size=world, dp_attention=True, context_parallel=True, cuda_graphs=False,
+                        max_prefill_tokens=128, enable_prefix_cache=False)
+    eng = Engine(build_model(cfg, ecfg, ps, sd, device=ps.device), ecfg, num_pages=16)
+    try:
+        r, got = first_logits(eng, cp_owner=1)
+        eng._drain_dp()
+    finally:
+        torch.cuda.synchronize()
+        dist.barrier(group=ps.cpu_group)
+    for obj in (ps.fused_ar, ps.fused_ep):
+        if obj is not None:
+            obj.check()
+    if rank != 1:
+        return rank, r.finish_reason, None, None
+    one = EngineConfig(cuda_graphs=False, enable_prefix_cache=False)
+    single = Engine(build_model(cfg, one, ParallelState(device=ps.device), sd, device=ps.device), one, num_pages=16)
+    _, want = first_logits(single)
+    return rank, r.finish_reason, got, want
+
+
+def test_cp2_prefill_matches_single_gpu():
+    """Context-parallel prefill of a 300-token prompt on 2 GPUs (rows split
+    round-robin, each layer's new fp8 cache rows all-gathered over NCCL,
+    MoE through the fused expert-parallel exchange): the owner's first-token
+    logits follow a 1-GPU prefill of the same prompt (fp8 noise only)."""
+    _needs(2)
+    res = run_ranks(_cp_rank, 2, timeout=600)
+    for rank, reason, got, want in res:
+        if rank == 1:
+            assert reason == "length"
+            assert _rel(got, want) < 0.15, _rel(got, want)
+        else:
+            assert reason == "context_parallel_peer"

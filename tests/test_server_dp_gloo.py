@@ -4,6 +4,8 @@ through rank 0; stopping ends the follower."""
 import threading
 import time
 
+import pytest
+
 from mp_util import run_ranks
 
 
@@ -22,7 +24,7 @@ class _Loop:
         self.events.append(item)
 
 
-def _rank(rank, world):
+def _rank(rank, world, cp=False):
     import torch
     from b200ds import build_model_from
     from b200ds.config import EngineConfig, tiny_config
@@ -33,7 +35,8 @@ def _rank(rank, world):
     from b200ds.server.openai import DPEngineWorker, follower_loop
     ps = init_parallel(backend="gloo", dp_attention=True)
     cfg = tiny_config()
-    ecfg = EngineConfig(page_size=8, cuda_graphs=False, tp_size=1, ep_size=world, dp_attention=True)
+    ecfg = EngineConfig(page_size=8, cuda_graphs=False, tp_size=1, ep_size=world, dp_attention=True,
+                        context_parallel=cp, cp_min_tokens=16, max_prefill_tokens=8)
     eng = Engine(build_model_from(cfg, ecfg, init_weights(cfg, 0), device="cpu", ps=ps), ecfg)
     if rank != 0:
         follower_loop(eng, ps)
@@ -41,6 +44,8 @@ def _rank(rank, world):
     w = DPEngineWorker(eng, None, ps).start()
     g = torch.Generator().manual_seed(9)
     prompts = torch.randint(0, cfg.vocab_size, (3, 10), generator=g).tolist()
+    if cp:      # one long prompt (assigned to rank 1) prefills on both ranks
+        prompts[1] = torch.randint(0, cfg.vocab_size, (27,), generator=g).tolist()
     loops = [_Loop() for _ in prompts]
     for p, lp in zip(prompts, loops):
         w.submit(p, SamplingParams(max_tokens=5), lp, lp)
@@ -53,14 +58,15 @@ def _rank(rank, world):
     return prompts, [[t for e in lp.events if e[0] == "tokens" for t in e[1]] for lp in loops]
 
 
-def test_dp_server_streams_every_ranks_tokens():
+@pytest.mark.parametrize("cp", [False, True])
+def test_dp_server_streams_every_ranks_tokens(cp):
     import torch
     from b200ds import build_model_from
     from b200ds.config import EngineConfig, tiny_config
     from b200ds.engine.engine import Engine
     from b200ds.engine.request import SamplingParams
     from b200ds.models.reference import init_weights
-    res = run_ranks(_rank, 2)
+    res = run_ranks(_rank, 2, cp)
     prompts, got = [r for r in res if r is not None][0]
     cfg = tiny_config()
     ecfg = EngineConfig(page_size=8, cuda_graphs=False)
