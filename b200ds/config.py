@@ -355,6 +355,8 @@ class EngineConfig:
     mixed_steps: bool = False        # prefill steps also advance running requests by one decode token
     context_parallel: bool = False   # DP attention: long prompts prefill on every rank (rows split round-robin)
     cp_min_tokens: int = 8192        # server: prompts at least this long take the context-parallel path
+    tbo: bool = False                # DP attention: two-batch overlap of prefill steps (MoE exchange vs compute)
+    tbo_min_tokens: int = 1024       # ... when the largest rank's step has at least this many rows
     prefill_tail: bool = True        # window-only late layers (V4 family) run only on each prompt's tail rows
     kv_cache_fraction: float = 0.85  # of free HBM after weights
     max_kv_pages: Optional[int] = None

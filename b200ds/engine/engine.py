@@ -268,13 +268,25 @@ class Engine:
         ntok = 0 if step is None else sum(len(c) for c in step.chunks) + sum(len(d) for d in drafts or [])
         nseq = 0 if step is None else len(step.reqs)
         prefill = step is not None and step.kind == "prefill"
-        lp = step is not None and _wants_lp(step.reqs)
+        lp = step is not None and (_wants_lp(step.reqs) or _wants_plp(step))
         v = torch.tensor([int(prefill), ntok, nseq, int(step is not None), int(lp), int(drafts is not None)],
                          dtype=torch.int64)
         dist.all_reduce(v, op=dist.ReduceOp.MAX, group=self.ps.cpu_group)
         any_prefill, max_tok, max_seq, any_work, any_lp, any_verify = (int(x) for x in v)
         if not any_work:
             return None
+        if (self.ecfg.tbo and any_prefill and not any_lp and not any_verify and self.mtp is None
+                and max_tok >= max(2, self.ecfg.tbo_min_tokens) and getattr(self.model, "supports_tbo", False)):
+            # every rank splits its rows into two micro-batches the same way
+            self.stats["tbo_steps"] = self.stats.get("tbo_steps", 0) + 1
+            seqs = [] if step is None else [{"tokens": ch, "start": st, "pages": r.pages}
+                                            for r, ch, st in zip(step.reqs, step.chunks, step.starts)]
+            logits = self._tbo_logits(seqs, max_tok)
+            if step is None:
+                return [], None
+            toks = self._sample(step, logits)
+            self._note_lp(step.reqs, logits, range(len(toks)), [[t] for t in toks], step.sample)
+            return toks, None
         seqs = [] if step is None else [{"tokens": ch, "start": st, "pages": r.pages}
                                         for r, ch, st in zip(step.reqs, step.chunks, step.starts)]
         if (not any_prefill and not any_lp and not any_verify and self.graphs is not None
@@ -297,6 +309,43 @@ class Engine:
         toks = self._sample(step, logits)
         self._note_lp(step.reqs, logits, range(len(toks)), [[t] for t in toks], step.sample)
         return toks, None
+
+    def _tbo_logits(self, seqs: List[dict], max_tok: int) -> Optional[torch.Tensor]:
+        """Two-batch overlap: this rank's rows split in two halves (a
+        sequence crossing the cut continues in the second micro-batch, whose
+        queries then read the first half's cache rows, written earlier in the
+        same layer); micro-batch k exchanges up to the agreed ceil / floor
+        half of the largest rank's rows; an empty half runs one dummy token on
+        the scratch page.  Returns the logits of each sequence's last row."""
+        T_r = sum(len(s["tokens"]) for s in seqs)
+        cut = (T_r + 1) // 2
+        halves: List[List[dict]] = [[], []]
+        ends = []
+        off = 0
+        for s in seqs:
+            toks, st, n = s["tokens"], s["start"], len(s["tokens"])
+            if off + n <= cut:
+                halves[0].append(s)
+            elif off >= cut:
+                halves[1].append(s)
+            else:
+                k = cut - off
+                halves[0].append({"tokens": toks[:k], "start": st, "pages": s["pages"]})
+                halves[1].append({"tokens": toks[k:], "start": st + k, "pages": s["pages"]})
+            m = 0 if off + n <= cut else 1
+            ends.append((m, len(halves[m]) - 1))
+            off += n
+        dummy = {"tokens": [0], "start": 0, "pages": [0]}
+        tmax = ((max_tok + 1) // 2, max_tok // 2)
+        fbs = []
+        for half, tm in zip(halves, tmax):
+            fb = build_batch(half or [dummy], self.ecfg.page_size, device="cpu")
+            fb.dp_tmax = max(tm, 1)
+            fbs.append(self._to_device(fb))
+        outs = self.model.forward_tbo(fbs)
+        if not seqs:
+            return None
+        return torch.stack([outs[m][j] for m, j in ends])
 
     def _eager_logits(self, step: Step, seqs: List[dict], dp_tmax: int = 0) -> torch.Tensor:
         """Eager forward of a step; returns the logits of each sequence's last

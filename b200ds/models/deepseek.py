@@ -33,6 +33,15 @@ from .batch import ForwardBatch
 from .rope import cos_sin_table
 
 
+def _drain(gen):
+    """Run a generator to completion; returns its return value."""
+    while True:
+        try:
+            next(gen)
+        except StopIteration as e:
+            return e.value
+
+
 class Linear:
     """y = x W^T with W either a float tensor (tiny/CPU) or an MXFP8Tensor."""
 
@@ -97,6 +106,7 @@ class LayerWeights:
 
 class DeepseekModel:
     supports_cp = True        # context-parallel prefill under DP attention (parallel/cp.py)
+    supports_tbo = True       # two-batch overlap of DP-attention prefill steps (forward_tbo)
 
     def __init__(self, cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState,
                  layers: List[LayerWeights], embed: torch.Tensor, final_ln: torch.Tensor,
@@ -264,6 +274,15 @@ class DeepseekModel:
             out = out + s
         return out
 
+    def _moe_dp_fused_ok(self, fb: ForwardBatch) -> bool:
+        """Whether this step's MoE exchange fits the symmetric-memory fused
+        path (native kernels, rows per rank within the dispatch buffers)."""
+        ps = self.ps
+        T_step = max(int(fb.dp_tmax or 0), fb.num_tokens)
+        ep, far = getattr(ps, "fused_ep", None), getattr(ps, "fused_ar", None)
+        return (self.device.type == "cuda" and ops.get_impl() == "native" and ep is not None and ep.supports(T_step)
+                and far is not None and far.supports(T_step))
+
     def _moe_dp(self, mw: MoEWeights, h, fb: ForwardBatch):
         """MoE under DP attention: this rank's T_r tokens (padded to the
         step's agreed T_step rows per rank) meet the routed experts of every
@@ -271,33 +290,59 @@ class DeepseekModel:
         expert owners, grouped GEMMs over the received tokens, and the
         combine + reduce-scatter fused into the next norm.  Host-collective
         path (CPU, baseline ops, steps larger than the symmetric buffers):
-        all-gather, local experts over all tokens, all-reduce, own slice."""
+        `_moe_dp_host`."""
         c, ps = self.cfg, self.ps
-        T_r = fb.num_tokens
-        T_step = max(int(fb.dp_tmax or 0), T_r)
-        out_dt = torch.float32 if self.device.type == "cpu" else torch.bfloat16
-        ep, far = getattr(ps, "fused_ep", None), getattr(ps, "fused_ar", None)
-        if (self.device.type == "cuda" and ops.get_impl() == "native" and ep is not None and ep.supports(T_step)
-                and far is not None and far.supports(T_step)):
+        if self._moe_dp_fused_ok(fb):
+            T_step = max(int(fb.dp_tmax or 0), fb.num_tokens)
+            out_dt = torch.bfloat16
             shared = None
             if mw.shared_gate_up is not None:
                 shared = self._fork(lambda: mw.shared_down(ops.gate_up_swiglu(h, mw.shared_gate_up),
                                                            out_dtype=out_dt), h)
             w, ids = ops.router(h, mw.gate, mw.bias, c)
-            part = ops.moe_experts_ep(h, w, ids, mw.experts, T_step, c.n_routed_experts, ep, far)
+            part = ops.moe_experts_ep(h, w, ids, mw.experts, T_step, c.n_routed_experts, ps.fused_ep, ps.fused_ar)
             if shared is not None:
                 part.add = self._join(shared)
             return part
+        return _drain(self._moe_dp_host(mw, h, fb))
+
+    def _moe_dp_host(self, mw: MoEWeights, h, fb: ForwardBatch):
+        """Host-collective MoE under DP attention, as a generator that yields
+        right after issuing each collective (asynchronously), so two-batch
+        overlap can run the other micro-batch's work meanwhile: all-gather of
+        every rank's rows, this rank's experts over all of them, then a
+        reduce-scatter (NCCL; all-reduce + own slice on gloo) back to the
+        owners; the shared expert runs during the reduction."""
+        import torch.distributed as dist
+        c, ps = self.cfg, self.ps
+        T_r = fb.num_tokens
+        T_step = max(int(fb.dp_tmax or 0), T_r)
+        out_dt = torch.float32 if self.device.type == "cpu" else torch.bfloat16
         x = ops.to_float(h)
         if T_step > T_r:
             x = torch.cat([x, x.new_zeros(T_step - T_r, x.shape[1])], 0)
-        g = ps.ep_all_gather(x.to(out_dt).contiguous())
+        x = x.to(out_dt).contiguous()
+        parts = [torch.empty_like(x) for _ in range(ps.ep_size)]
+        work = dist.all_gather(parts, x, group=ps.ep_group, async_op=True)
+        yield
+        work.wait()
+        g = torch.cat(parts, 0)
         w, ids = ops.router(g, mw.gate, mw.bias, c)
         part = ops.moe_experts(g, w, ids, mw.experts, out_dtype=torch.float32, n_experts_total=c.n_routed_experts)
-        ps.ep_all_reduce(part)
-        out = part[ps.ep_rank * T_step: ps.ep_rank * T_step + T_r]
+        if dist.get_backend(ps.ep_group) == "nccl":
+            out = torch.empty(T_step, part.shape[1], dtype=part.dtype, device=part.device)
+            work = dist.reduce_scatter_tensor(out, part.contiguous(), group=ps.ep_group, async_op=True)
+        else:
+            out = None
+            work = dist.all_reduce(part, group=ps.ep_group, async_op=True)
+        shared = None
         if mw.shared_gate_up is not None:
-            out = out + mw.shared_down(ops.gate_up_swiglu(h, mw.shared_gate_up), out_dtype=torch.float32).float()
+            shared = mw.shared_down(ops.gate_up_swiglu(h, mw.shared_gate_up), out_dtype=torch.float32).float()
+        yield
+        work.wait()
+        out = out[:T_r] if out is not None else part[ps.ep_rank * T_step: ps.ep_rank * T_step + T_r]
+        if shared is not None:
+            out = out + shared
         return out.to(out_dt)
 
     # ------------------------------------------------------------------
@@ -372,6 +417,36 @@ class DeepseekModel:
         x0: the initial residual stream instead of the token embeddings (the
         MTP module).  The pre-norm final residual of every row is kept in
         `last_residual` (the speculative draft's input)."""
+        return _drain(self._hidden_steps(fb, x0))
+
+    @torch.no_grad()
+    def forward_tbo(self, fbs: List[ForwardBatch]) -> List[torch.Tensor]:
+        """Two-batch overlap (DP attention prefill): the micro-batches in
+        `fbs` run the layer stack interleaved, each handing over to the next
+        right after it issues a collective of the host-collective MoE
+        exchange, so one micro-batch's all-gather / reduce-scatter runs
+        (NCCL's stream, asynchronously) while the other computes.  Each
+        micro-batch's collectives are issued in the same order on every rank.
+        Returns the logits of each micro-batch's sequences.
+
+        Reference parity: SGLang's two-batch overlap for expert-parallel
+        batches (`_can_run_tbo`, `_forward_layers_tbo`, fork_loop.py:121,
+        151-158)."""
+        gens = [self._hidden_steps(fb) for fb in fbs]
+        hs = [None] * len(gens)
+        live = list(range(len(gens)))
+        while live:
+            for k in list(live):
+                try:
+                    next(gens[k])
+                except StopIteration as e:
+                    hs[k] = e.value
+                    live.remove(k)
+        return [ops.lm_head_logits(self._last_hidden(h, fb), self.lm_head, self.ps) for h, fb in zip(hs, fbs)]
+
+    def _hidden_steps(self, fb: ForwardBatch, x0: Optional[torch.Tensor] = None):
+        """`_hidden` as a generator: yields after each asynchronous collective
+        of a host-collective MoE exchange (none on the fused paths)."""
         c = self.cfg
         tr = self.tracer
         tr.reset()
@@ -385,7 +460,10 @@ class DeepseekModel:
             h, residual = ops.allreduce_add_rmsnorm(a, residual, lw.post_ln, c.rms_norm_eps,
                                                     self.ps, "tp_attn", self._ffn_first_linear(lw))
             tr.mark(f"L{i}.ffn")
-            f = self._ffn(i, lw, h, fb)
+            if self.dp and isinstance(lw.ffn, MoEWeights) and not self._moe_dp_fused_ok(fb):
+                f = yield from self._moe_dp_host(lw.ffn, h, fb)
+            else:
+                f = self._ffn(i, lw, h, fb)
             nxt = self.layers[i + 1] if i + 1 < len(self.layers) else None
             # under DP attention only the fused expert-parallel partial still
             # needs a collective; every other FFN output is already this rank's

@@ -1031,6 +1031,8 @@ def main(argv=None):
     ap.add_argument("--context-parallel", action="store_true",
                     help="with --dp-attention: long prompts prefill on every rank")
     ap.add_argument("--cp-min-tokens", type=int, default=8192, help="shortest prompt that prefills context-parallel")
+    ap.add_argument("--tbo", action="store_true",
+                    help="with --dp-attention: two-batch overlap of prefill steps (MoE exchange vs compute)")
     ap.add_argument("--extend-graphs", action="store_true", help="replay prefill chunks from CUDA graphs")
     ap.add_argument("--page-size", type=int, default=64, help="tokens per KV page")
     ap.add_argument("--max-prefill-tokens", type=int, default=16384, help="chunked-prefill budget per step")
@@ -1068,7 +1070,7 @@ def main(argv=None):
                         graph_batch_sizes=tuple(int(x) for x in args.graph_batch_sizes.split(",") if x),
                         prefill_tail=not args.no_prefill_tail, comm_impl=args.comm,
                         schedule_policy=args.schedule_policy, host_kv_pages=args.host_kv_pages,
-                        context_parallel=args.context_parallel, cp_min_tokens=args.cp_min_tokens)
+                        context_parallel=args.context_parallel, cp_min_tokens=args.cp_min_tokens, tbo=args.tbo)
     eng = load_engine(args.model, weights=args.weights, ecfg=ecfg)
     tok = load_tokenizer(args.model)
     eng.tokenizer = tok

@@ -96,3 +96,35 @@ def test_dp2_speculative_ngram_matches_single():
     assert sum(r[2] for r in res) > 0                    # drafts were proposed and verified
     for mine, toks, _, _ in res:
         assert toks == [ref[i] for i in mine]
+
+
+def _tbo_rank(rank, world):
+    from b200ds import build_model_from
+    from b200ds.config import EngineConfig, tiny_config
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.reference import init_weights
+    from b200ds.parallel.state import init_parallel
+    ps = init_parallel(backend="gloo", dp_attention=True)
+    cfg = tiny_config()
+    ecfg = EngineConfig(page_size=8, cuda_graphs=False, tp_size=1, ep_size=world, dp_attention=True,
+                        tbo=True, tbo_min_tokens=4)
+    eng = Engine(build_model_from(cfg, ecfg, init_weights(cfg, 0), device="cpu", ps=ps), ecfg)
+    mine = [i for i in range(3) if i % world == rank]
+    outs = eng.generate([_prompts(cfg)[i] for i in mine], [SamplingParams(max_tokens=_max_tokens()[i]) for i in mine])
+    return mine, [o.token_ids for o in outs], eng.stats.get("tbo_steps", 0)
+
+
+def test_dp2_two_batch_overlap_matches_single():
+    """Two-batch overlap of DP prefill steps: each rank's rows run as two
+    micro-batches interleaved at the MoE exchange's asynchronous collectives
+    (rank 0's 20 + 13 rows split inside the second prompt, so its second half
+    reads the first half's cache rows; rank 1's prompt alone); tokens equal a
+    single-process run."""
+    from b200ds.config import EngineConfig, tiny_config
+    cfg = tiny_config()
+    ref, _ = _run(cfg, EngineConfig(page_size=8, cuda_graphs=False), _prompts(cfg), _max_tokens())
+    res = run_ranks(_tbo_rank, 2)
+    for mine, toks, tbo_steps in res:
+        assert tbo_steps >= 1
+        assert toks == [ref[i] for i in mine]

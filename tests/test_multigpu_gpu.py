@@ -301,3 +301,55 @@ def test_cp2_prefill_matches_single_gpu():
             assert _rel(got, want) < 0.15, _rel(got, want)
         else:
             assert reason == "context_parallel_peer"
+
+
+def _tbo_rank(rank, world):
+    import torch
+    import torch.distributed as dist
+    from b200ds import ops
+    from b200ds.config import EngineConfig, small_gpu_config
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.loader import build_model
+    from b200ds.models.reference import init_weights
+    from b200ds.parallel.state import ParallelState, init_parallel
+    ps = init_parallel(backend="nccl", dp_attention=True, timeout_s=60)
+    ops.set_impl("native")
+    cfg = small_gpu_config(num_attention_heads=16)
+    sd = init_weights(cfg, 0)
+    g = torch.Generator().manual_seed(31 + rank)
+    prompt = torch.randint(0, cfg.vocab_size, (40 if rank == 0 else 25,), generator=g).tolist()
+
+    def first_logits(eng):
+        seen = []
+        orig = eng._sample
+        eng._sample = lambda st, lg: seen.append(lg.float().cpu()) or orig(st, lg)
+        r = eng.add_request(prompt, SamplingParams(max_tokens=2))
+        while not r.finished:
+            eng.step()
+        return seen[0]
+
+    # NCCL exchange (the host-collective path the overlap interleaves)
+    ecfg = EngineConfig(tp_size=1, ep_size=world, dp_attention=True, comm_impl="nccl", cuda_graphs=False,
+                        tbo=True, tbo_min_tokens=2, enable_prefix_cache=False)
+    eng = Engine(build_model(cfg, ecfg, ps, sd, device=ps.device), ecfg, num_pages=8)
+    try:
+        got = first_logits(eng)
+        eng._drain_dp()
+    finally:
+        torch.cuda.synchronize()
+        dist.barrier(group=ps.cpu_group)
+    one = EngineConfig(cuda_graphs=False, enable_prefix_cache=False)
+    single = Engine(build_model(cfg, one, ParallelState(device=ps.device), sd, device=ps.device), one, num_pages=8)
+    return rank, eng.stats.get("tbo_steps", 0), got, first_logits(single)
+
+
+def test_dp2_two_batch_overlap_gpu():
+    """Two-batch overlap on 2 GPUs: each rank's prefill rows run as two
+    micro-batches whose NCCL all-gather / reduce-scatter overlap the other
+    micro-batch's kernels; first-token logits follow a 1-GPU run."""
+    _needs(2)
+    res = run_ranks(_tbo_rank, 2, timeout=600)
+    for rank, steps, got, want in res:
+        assert steps >= 1
+        assert _rel(got, want) < 0.15, (rank, _rel(got, want))
