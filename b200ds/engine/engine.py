@@ -968,6 +968,8 @@ class Engine:
         m = self.model
         fb = self._to_device(fb)
         h = m._hidden(fb)
+        if isinstance(h, tuple):          # the V4 family returns (hidden, batch)
+            h, fb = h
         r.cached = start + n
         self.stats["steps"] += 1
         self.stats["prefill_tokens"] += own

@@ -81,6 +81,8 @@ class _Partial:
 
 
 class DeepseekV4Model:
+    supports_cp = True        # context-parallel prefill under DP attention (parallel/cp.py)
+
     def __init__(self, cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState, layers: List[V4LayerWeights],
                  embed: torch.Tensor, hc_head: HcWeights, final_ln: torch.Tensor, lm_head, device,
                  kv_dtype=torch.float8_e4m3fn):
@@ -221,6 +223,7 @@ class DeepseekV4Model:
         qo = aw.wq_b(q_lat, out_dtype=od)
         q = qo[:, : self.heads * L].view(T, self.heads, L)
         topk, comp = None, None
+        cp_done = fb.cp is None
         if c.is_window_layer(i):
             # window-only layer: the selection is the last late_window positions
             # (built on the device from the positions, graph-safe)
@@ -239,7 +242,13 @@ class DeepseekV4Model:
                 # compressed rows of the blocks this step completes, then the
                 # window + top compressed blocks
                 cc = self.comp[i]
-                ops.compress_store(qkv[:, base + hd + nh], aw.comp_bias, fb, cc["ratio"], self.kv_cache[i],
+                g, cfb = qkv[:, base + hd + nh], fb
+                if not cp_done:
+                    # context parallel: every rank's rows and gate logits first;
+                    # then each rank compresses the chunk's blocks itself
+                    g, cfb = self._cp_gather(i, fb, g), fb.cp.whole(fb)
+                    cp_done = True
+                ops.compress_store(g, aw.comp_bias, cfb, cc["ratio"], self.kv_cache[i],
                                    self.kv_scale[i], self.ix_cache[i], self.ix_scale[i], cc["gate"], cc["kv"],
                                    cc["ik"], cc["iks"], self.page_size)
                 topk = ops.indexer_topk_compressed(q_ix, w_ix, (nh * hd) ** -0.5, self.rope_table, cc["ik"],
@@ -247,13 +256,30 @@ class DeepseekV4Model:
                                                    c.index_swa)
                 comp = (cc["kv"], cc["ratio"])
             else:
+                if not cp_done:
+                    self._cp_gather(i, fb)
+                    cp_done = True
                 topk = ops.indexer_topk(q_ix, w_ix, (nh * hd) ** -0.5, self.rope_table, self.ix_cache[i],
                                         self.ix_scale[i], fb, self.page_size, c.index_topk, c.index_swa)
+        if not cp_done:
+            self._cp_gather(i, fb)
         o = ops.mqa_attention(q, self.kv_cache[i], self.kv_scale[i], fb, c.softmax_scale, self.page_size, aw.sink,
                               self.rope_table, rd, topk, comp=comp)
         z = ops.absorb_o(o.reshape(T, self.groups, -1), aw.wo_a, quantize=aw.wo_b.quantized)
         y = aw.wo_b(z, out_dtype=od)
         return self._reduce(y)
+
+    def _cp_gather(self, i: int, fb: ForwardBatch, gate: Optional[torch.Tensor] = None):
+        """Context-parallel chunk: every rank's new cache rows of layer i (the
+        latent row; the indexer key + scale where the layer stores one) into
+        this rank's cache before any query of the chunk attends; a compressed
+        layer's gate logits travel along (returned for the whole chunk)."""
+        from ..parallel.cp import gather_rows
+        c = self.cfg
+        bufs = [self.kv_cache[i]]
+        if c.index_n_heads and not c.is_window_layer(i):
+            bufs += [self.ix_cache[i], self.ix_scale[i]]
+        return gather_rows(bufs, fb, self.ps, extra=gate)
 
     def _ffn(self, i: int, lw: V4LayerWeights, h, fb: ForwardBatch) -> torch.Tensor:
         c = self.cfg
@@ -315,6 +341,11 @@ class DeepseekV4Model:
         X, ss = ops.hc_embed(self.embed, fb.input_ids, c.hc_mult)
         eids = None
         if c.engram_layers:
+            if fb.cp is not None:
+                # context parallel: a row's n-gram predecessors sit on other
+                # ranks; the whole chunk's tokens go to the token cache first
+                w = fb.cp.whole(fb)
+                self.tok_cache[w.out_slots] = w.input_ids.to(self.tok_cache.dtype)
             eids = ops.engram_ids(fb, self.tok_cache, c, self.engram_mults, self.page_size)
         self.aux = []
         self.tail_skipped = 0

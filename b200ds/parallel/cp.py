@@ -22,7 +22,8 @@ fork_attn.py:101,303-307).
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import List, Sequence
+from types import SimpleNamespace
+from typing import List, Optional, Sequence
 
 import torch
 
@@ -44,11 +45,14 @@ class CPLayout:
     """How one chunk's cache rows travel: every rank contributes `counts[q]`
     rows padded to `tmax`; row j of rank q belongs to position start + q +
     j * W.  `src_rows` index the gathered [W * tmax] rows in chunk-position
-    order and `dst_slots` are this rank's cache slots of those positions."""
+    order and `dst_slots` are this rank's cache slots of those positions;
+    `ids` are the chunk's token ids in position order."""
     counts: List[int]
     tmax: int
+    start: int
     src_rows: torch.Tensor       # [n] int64
     dst_slots: torch.Tensor      # [n] int64
+    ids: torch.Tensor            # [n] int32
     _dev: dict = None
 
     def on(self, device):
@@ -61,8 +65,27 @@ class CPLayout:
                               self.dst_slots.to(device, non_blocking=True))
         return self._dev[key]
 
+    def whole(self, fb: ForwardBatch) -> SimpleNamespace:
+        """The whole chunk as one sequence (positions, slots, ids, q_seq,
+        block table on fb's device): what a step that runs on every row of
+        the chunk at once reads (the compressor's block means, the token
+        cache of the n-gram hashes)."""
+        dev = fb.out_slots.device
+        key = "whole:" + str(dev)
+        if self._dev is None:
+            self._dev = {}
+        if key not in self._dev:
+            n = int(self.ids.shape[0])
+            self._dev[key] = SimpleNamespace(
+                positions=torch.arange(self.start, self.start + n, dtype=torch.int32).to(dev),
+                out_slots=self.on(dev)[1], input_ids=self.ids.to(dev), q_seq=torch.zeros(n, dtype=torch.int32,
+                                                                                          device=dev),
+                block_table=fb.block_table)
+        return self._dev[key]
 
-def layout(start: int, n: int, world: int, pages: Sequence[int], page_size: int) -> CPLayout:
+
+def layout(start: int, n: int, world: int, pages: Sequence[int], page_size: int,
+           tokens: Sequence[int] = ()) -> CPLayout:
     counts = [len(range(q, n, world)) for q in range(world)]
     tmax = max(max(counts), 1)
     src, pos = [], []
@@ -74,7 +97,9 @@ def layout(start: int, n: int, world: int, pages: Sequence[int], page_size: int)
     src = [src[k] for k in order]
     pos = [pos[k] for k in order]
     slots = [pages[p // page_size] * page_size + p % page_size for p in pos]
-    return CPLayout(counts, tmax, torch.tensor(src, dtype=torch.int64), torch.tensor(slots, dtype=torch.int64))
+    ids = [tokens[p] for p in pos] if tokens else [0] * n
+    return CPLayout(counts, tmax, start, torch.tensor(src, dtype=torch.int64), torch.tensor(slots, dtype=torch.int64),
+                    torch.tensor(ids, dtype=torch.int32))
 
 
 def build_cp_batch(prompt: Sequence[int], start: int, n: int, world: int, rank: int, pages: Sequence[int],
@@ -106,7 +131,7 @@ def build_cp_batch(prompt: Sequence[int], start: int, n: int, world: int, rank: 
         max_q_len=T,
         max_seq_len=seq_len,
     )
-    fb.cp = layout(start, n, world, pages, page_size)
+    fb.cp = layout(start, n, world, pages, page_size, prompt)
     fb.dp_tmax = fb.cp.tmax
     return fb
 
@@ -116,15 +141,23 @@ def _rows_u8(buf: torch.Tensor) -> torch.Tensor:
     return buf.view(torch.uint8).reshape(buf.shape[0], -1)
 
 
-def gather_rows(bufs: Sequence[torch.Tensor], fb: ForwardBatch, ps) -> None:
+def gather_rows(bufs: Sequence[torch.Tensor], fb: ForwardBatch, ps,
+                extra: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
     """All-gather this chunk's freshly stored cache rows of every buffer in
     `bufs` (one collective for all of them) and write them into this rank's
-    slots, so each rank's cache holds the whole chunk."""
+    slots, so each rank's cache holds the whole chunk.  `extra` (one fp32
+    value per row of this rank) travels along; returned for the whole chunk
+    in position order."""
     cp: CPLayout = fb.cp
     views = [_rows_u8(b) for b in bufs]
     widths = [v.shape[1] for v in views]
     own = fb.out_slots
-    pack = torch.cat([v[own] for v in views], 1)
+    cols = [v[own] for v in views]
+    if extra is not None:
+        e = torch.empty(extra.shape[0], dtype=torch.float32, device=extra.device)
+        e.copy_(extra)          # fresh stride-1 storage (a strided column of one row counts as contiguous)
+        cols.append(e.view(torch.uint8).reshape(-1, 4))
+    pack = torch.cat(cols, 1)
     if pack.shape[0] < cp.tmax:
         pack = torch.cat([pack, pack.new_zeros(cp.tmax - pack.shape[0], pack.shape[1])], 0)
     elif pack.shape[0] > cp.tmax:        # a dummy row on a rank with no rows: tmax >= 1 already
@@ -136,3 +169,6 @@ def gather_rows(bufs: Sequence[torch.Tensor], fb: ForwardBatch, ps) -> None:
     for v, w in zip(views, widths):
         v[dst] = rows[:, off:off + w]
         off += w
+    if extra is None:
+        return None
+    return rows[:, off:off + 4].contiguous().view(torch.float32).reshape(-1)

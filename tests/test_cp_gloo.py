@@ -134,3 +134,57 @@ def test_cp_layout_round_robin():
     assert holder_of_last(10, 3) == 0
     empty = build_cp_batch(list(range(20)), 0, 1, 2, 1, pages, 4)     # rank 1 has no rows
     assert empty.out_slots.tolist() == [0] and empty.cp.counts == [1, 0]
+
+
+def _v4_cfg(compressed: bool):
+    from b200ds.config import tiny_v4_config
+    if compressed:      # indexer, compressed blocks at ratios 2 / 4, Engram at layer 1
+        return tiny_v4_config(index_n_heads=8, index_head_dim=32, index_topk=6, index_swa=4,
+                              compress_ratios=(0, 2, 4), compress_topk=4)
+    return tiny_v4_config()
+
+
+def _v4_single(cfg, prompt, maxt):
+    from b200ds import build_model_from
+    from b200ds.config import EngineConfig
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.reference_v4 import init_weights_v4
+    ecfg = EngineConfig(page_size=8, cuda_graphs=False, enable_prefix_cache=False)
+    eng = Engine(build_model_from(cfg, ecfg, init_weights_v4(cfg, 0), device="cpu"), ecfg)
+    return eng.generate([prompt], SamplingParams(max_tokens=maxt))[0].token_ids
+
+
+def _v4_rank(rank, world, compressed):
+    from b200ds import build_model_from
+    from b200ds.config import EngineConfig
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.reference_v4 import init_weights_v4
+    from b200ds.parallel.state import init_parallel
+    ps = init_parallel(backend="gloo", dp_attention=True)
+    cfg = _v4_cfg(compressed)
+    ecfg = EngineConfig(page_size=8, cuda_graphs=False, tp_size=1, ep_size=world, dp_attention=True,
+                        context_parallel=True, max_prefill_tokens=8)
+    eng = Engine(build_model_from(cfg, ecfg, init_weights_v4(cfg, 0), device="cpu", ps=ps), ecfg)
+    r = eng.add_request(_prompts(cfg)[0], SamplingParams(max_tokens=6), cp_owner=1)
+    while not r.finished:
+        eng.step()
+    eng._drain_dp()
+    return rank, r.output, r.finish_reason
+
+
+@pytest.mark.parametrize("compressed", [False, True])
+def test_cp2_v4_prefill_matches_single(compressed):
+    """The V4 family under context parallelism: each rank's n-gram hashes
+    read the whole chunk's tokens from the token cache, compressed layers
+    gather the gate logits with the cache rows and every rank compresses the
+    chunk's blocks; the owner's tokens equal a single-process run."""
+    cfg = _v4_cfg(compressed)
+    want = _v4_single(cfg, _prompts(cfg)[0], 6)
+    res = run_ranks(_v4_rank, 2, compressed)
+    for rank, out, reason in res:
+        if rank == 1:
+            assert out == want and reason == "length"
+        else:
+            assert out == [] and reason == "context_parallel_peer"
