@@ -157,8 +157,8 @@ class Engine:
                     cp_owner: Optional[int] = None) -> Request:
         """Queue a request.  cp_owner (context_parallel engines): prefill the
         prompt on every rank and decode it on rank cp_owner; every rank must
-        add it, in the same order relative to its other context-parallel
-        requests.  On the other ranks the returned request finishes after the
+        add it between the same two steps, in the same order relative to its
+        other context-parallel requests.  On the other ranks the returned request finishes after the
         prefill with finish_reason "context_parallel_peer" and no tokens."""
         if isinstance(prompt, str):
             assert self.tokenizer is not None, "text prompts need a tokenizer"
@@ -474,7 +474,7 @@ class Engine:
 
     def step(self) -> List[Request]:
         """Run one scheduler step; returns requests that finished."""
-        if self.cp and self._cp_agree():
+        if self._cp_pending() and self._cp_agree():
             self._step_lp = {}
             return self._cp_step()
         st = self.sched.next_step()
@@ -876,7 +876,7 @@ class Engine:
         if self.dp:
             # keep stepping (as an idle rank) until every rank is done
             while True:
-                if self.cp and self._cp_agree():
+                if self._cp_pending() and self._cp_agree():
                     self._cp_step()
                     continue
                 if self._dp_forward(None) is None:
@@ -895,6 +895,14 @@ class Engine:
             raise ValueError("context-parallel requests do not return prompt log-probabilities")
         if not 0 <= owner < self.ps.ep_size:
             raise ValueError(f"cp_owner {owner} is not a rank of the {self.ps.ep_size}-rank group")
+
+    def _cp_pending(self) -> bool:
+        """Whether the context-parallel queue holds a request.  The queue is
+        the same on every rank (requests are added on all ranks between the
+        same two steps and leave together), so ranks with an empty queue skip
+        the agreement together and steps without context-parallel work cost
+        no extra collective."""
+        return self.cp and (self._cp_cur is not None or bool(self._cp_wait))
 
     def _cp_all(self) -> List[Request]:
         return ([self._cp_cur] if self._cp_cur is not None else []) + list(self._cp_wait)
