@@ -107,6 +107,7 @@ class LayerWeights:
 class DeepseekModel:
     supports_cp = True        # context-parallel prefill under DP attention (parallel/cp.py)
     supports_tbo = True       # two-batch overlap of DP-attention prefill steps (forward_tbo)
+    _tbo_live = False         # forward_tbo is interleaving micro-batches
 
     def __init__(self, cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState,
                  layers: List[LayerWeights], embed: torch.Tensor, final_ln: torch.Tensor,
@@ -322,24 +323,29 @@ class DeepseekModel:
         if T_step > T_r:
             x = torch.cat([x, x.new_zeros(T_step - T_r, x.shape[1])], 0)
         x = x.to(out_dt).contiguous()
+        # asynchronous only while two micro-batches interleave (never inside a
+        # graph capture); otherwise the collectives complete in place
+        overlap = self._tbo_live and not (x.is_cuda and torch.cuda.is_current_stream_capturing())
         parts = [torch.empty_like(x) for _ in range(ps.ep_size)]
-        work = dist.all_gather(parts, x, group=ps.ep_group, async_op=True)
+        work = dist.all_gather(parts, x, group=ps.ep_group, async_op=overlap)
         yield
-        work.wait()
+        if overlap:
+            work.wait()
         g = torch.cat(parts, 0)
         w, ids = ops.router(g, mw.gate, mw.bias, c)
         part = ops.moe_experts(g, w, ids, mw.experts, out_dtype=torch.float32, n_experts_total=c.n_routed_experts)
         if dist.get_backend(ps.ep_group) == "nccl":
             out = torch.empty(T_step, part.shape[1], dtype=part.dtype, device=part.device)
-            work = dist.reduce_scatter_tensor(out, part.contiguous(), group=ps.ep_group, async_op=True)
+            work = dist.reduce_scatter_tensor(out, part.contiguous(), group=ps.ep_group, async_op=overlap)
         else:
             out = None
-            work = dist.all_reduce(part, group=ps.ep_group, async_op=True)
+            work = dist.all_reduce(part, group=ps.ep_group, async_op=overlap)
         shared = None
         if mw.shared_gate_up is not None:
             shared = mw.shared_down(ops.gate_up_swiglu(h, mw.shared_gate_up), out_dtype=torch.float32).float()
         yield
-        work.wait()
+        if overlap:
+            work.wait()
         out = out[:T_r] if out is not None else part[ps.ep_rank * T_step: ps.ep_rank * T_step + T_r]
         if shared is not None:
             out = out + shared
@@ -435,13 +441,17 @@ class DeepseekModel:
         gens = [self._hidden_steps(fb) for fb in fbs]
         hs = [None] * len(gens)
         live = list(range(len(gens)))
-        while live:
-            for k in list(live):
-                try:
-                    next(gens[k])
-                except StopIteration as e:
-                    hs[k] = e.value
-                    live.remove(k)
+        self._tbo_live = True
+        try:
+            while live:
+                for k in list(live):
+                    try:
+                        next(gens[k])
+                    except StopIteration as e:
+                        hs[k] = e.value
+                        live.remove(k)
+        finally:
+            self._tbo_live = False
         return [ops.lm_head_logits(self._last_hidden(h, fb), self.lm_head, self.ps) for h, fb in zip(hs, fbs)]
 
     def _hidden_steps(self, fb: ForwardBatch, x0: Optional[torch.Tensor] = None):
