@@ -965,7 +965,9 @@ class Engine:
         """Prefill the next chunk of the context-parallel head on every rank
         (this rank's rows: positions start + rank + k * W); after the last
         chunk the owner samples the first token and the request joins its
-        running set, the other ranks release their copy of the cache."""
+        running set (which may then hold max_num_seqs plus the
+        context-parallel requests it decodes), the other ranks release their
+        copy of the cache."""
         from ..parallel.cp import build_cp_batch, holder_of_last
         r = self._cp_cur
         W, me = self.ps.ep_size, self.ps.ep_rank
