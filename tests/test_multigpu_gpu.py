@@ -353,3 +353,60 @@ def test_dp2_two_batch_overlap_gpu():
     for rank, steps, got, want in res:
         assert steps >= 1
         assert _rel(got, want) < 0.15, (rank, _rel(got, want))
+
+
+def _cp_v4_rank(rank, world):
+    import torch
+    import torch.distributed as dist
+    from b200ds import build_model_from, ops
+    from b200ds.config import EngineConfig, small_v4_gpu_config
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.reference_v4 import init_weights_v4
+    from b200ds.parallel.state import ParallelState, init_parallel
+    ps = init_parallel(backend="nccl", dp_attention=True, timeout_s=60)
+    ops.set_impl("native")
+    cfg = small_v4_gpu_config()
+    sd = init_weights_v4(cfg, 0)
+    g = torch.Generator().manual_seed(23)
+    prompt = torch.randint(0, cfg.vocab_size, (200,), generator=g).tolist()
+
+    def first_logits(eng, **kw):
+        seen = []
+        orig = eng._sample
+        eng._sample = lambda st, lg: seen.append(lg.float().cpu()) or orig(st, lg)
+        r = eng.add_request(prompt, SamplingParams(max_tokens=2), **kw)
+        while not r.finished:
+            eng.step()
+        return r, (seen[0] if seen else None)
+
+    ecfg = EngineConfig(tp_size=1, ep_size=world, dp_attention=True, context_parallel=True, cuda_graphs=False,
+                        max_prefill_tokens=64, enable_prefix_cache=False)
+    eng = Engine(build_model_from(cfg, ecfg, sd, device=ps.device, ps=ps), ecfg, num_pages=8)
+    try:
+        r, got = first_logits(eng, cp_owner=0)
+        eng._drain_dp()
+    finally:
+        torch.cuda.synchronize()
+        dist.barrier(group=ps.cpu_group)
+    if rank != 0:
+        return rank, r.finish_reason, None, None
+    one = EngineConfig(cuda_graphs=False, enable_prefix_cache=False)
+    single = Engine(build_model_from(cfg, one, sd, device=ps.device, ps=ParallelState(device=ps.device)), one,
+                    num_pages=8)
+    _, want = first_logits(single)
+    return rank, r.finish_reason, got, want
+
+
+def test_cp2_v4_prefill_matches_single_gpu():
+    """Context-parallel prefill of the V4 family on 2 GPUs (n-gram hashes over
+    the whole chunk's token cache, mHC per row, chunks of 128 rows): the
+    owner's first-token logits follow a 1-GPU prefill (fp8 noise only)."""
+    _needs(2)
+    res = run_ranks(_cp_v4_rank, 2, timeout=600)
+    for rank, reason, got, want in res:
+        if rank == 0:
+            assert reason == "length"
+            assert _rel(got, want) < 0.15, _rel(got, want)
+        else:
+            assert reason == "context_parallel_peer"
