@@ -1,6 +1,7 @@
 """DP attention + EP MoE on CPU (gloo, 2 ranks): each rank serves its own
 requests, the MoE exchanges tokens between ranks, and every request's tokens
 and prefill logits must match a single-process run of all requests."""
+import pytest
 import torch
 
 from mp_util import run_ranks
@@ -98,7 +99,7 @@ def test_dp2_speculative_ngram_matches_single():
         assert toks == [ref[i] for i in mine]
 
 
-def _tbo_rank(rank, world):
+def _tbo_rank(rank, world, idle_rank1=False):
     from b200ds import build_model_from
     from b200ds.config import EngineConfig, tiny_config
     from b200ds.engine.engine import Engine
@@ -110,12 +111,16 @@ def _tbo_rank(rank, world):
     ecfg = EngineConfig(page_size=8, cuda_graphs=False, tp_size=1, ep_size=world, dp_attention=True,
                         tbo=True, tbo_min_tokens=4)
     eng = Engine(build_model_from(cfg, ecfg, init_weights(cfg, 0), device="cpu", ps=ps), ecfg)
-    mine = [i for i in range(3) if i % world == rank]
+    mine = [i for i in range(3) if (rank == 0 if idle_rank1 else i % world == rank)]
+    if not mine:            # an idle rank: dummy micro-batches in every overlapped step
+        eng._drain_dp()
+        return mine, [], eng.stats.get("tbo_steps", 0)
     outs = eng.generate([_prompts(cfg)[i] for i in mine], [SamplingParams(max_tokens=_max_tokens()[i]) for i in mine])
     return mine, [o.token_ids for o in outs], eng.stats.get("tbo_steps", 0)
 
 
-def test_dp2_two_batch_overlap_matches_single():
+@pytest.mark.parametrize("idle_rank1", [False, True])
+def test_dp2_two_batch_overlap_matches_single(idle_rank1):
     """Two-batch overlap of DP prefill steps: each rank's rows run as two
     micro-batches interleaved at the MoE exchange's asynchronous collectives
     (rank 0's 20 + 13 rows split inside the second prompt, so its second half
@@ -124,7 +129,7 @@ def test_dp2_two_batch_overlap_matches_single():
     from b200ds.config import EngineConfig, tiny_config
     cfg = tiny_config()
     ref, _ = _run(cfg, EngineConfig(page_size=8, cuda_graphs=False), _prompts(cfg), _max_tokens())
-    res = run_ranks(_tbo_rank, 2)
+    res = run_ranks(_tbo_rank, 2, idle_rank1)
     for mine, toks, tbo_steps in res:
         assert tbo_steps >= 1
         assert toks == [ref[i] for i in mine]
