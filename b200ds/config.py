@@ -192,14 +192,16 @@ class ModelConfig:
     # ---- io ----------------------------------------------------------------
     @classmethod
     def from_hf(cls, path_or_dict) -> "ModelConfig":
-        """Build from a Hugging Face DeepSeek-V3 `config.json` (path or dict)."""
+        """Build from a Hugging Face DeepSeek `config.json` (path or dict); a
+        config written by `to_dict` (V4-family fields included) round-trips."""
         if isinstance(path_or_dict, dict):
             d = path_or_dict
         else:
             with open(path_or_dict) as f:
                 d = json.load(f)
         names = {f.name for f in dataclasses.fields(cls)}
-        kw = {k: v for k, v in d.items() if k in names}
+        # JSON lists of the tuple-valued fields (layer lists, ratios) back to tuples
+        kw = {k: (tuple(v) if isinstance(v, list) else v) for k, v in d.items() if k in names}
         if "index_n_heads" not in d and "index_head_dim" in d:
             kw["index_n_heads"] = 64
         qc = d.get("quantization_config") or {}

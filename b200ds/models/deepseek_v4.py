@@ -449,7 +449,14 @@ def build_model_v4(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState, sd: 
     wdt = torch.bfloat16 if dev.type == "cuda" else torch.float32
 
     def get(name) -> torch.Tensor:
-        return sd[name].float()
+        t = sd[name]
+        si = sd.get(name + "_scale_inv")
+        if si is None:
+            return t.float()
+        from ..ops.quant import dequant_blocked
+        if dev.type == "cuda":       # fp8 bytes cross the host link; dequantize on the device
+            t, si = t.to(dev), si.to(dev)
+        return dequant_blocked(t, si)
 
     def split(t, dim, n, r):
         return t.chunk(n, dim)[r].contiguous() if n > 1 else t

@@ -1,6 +1,7 @@
-"""Weight construction: HF state dicts / safetensors checkpoints (fp8 with
-128x128 `weight_scale_inv` block scales) and random init generated directly
-in each rank's shard, in the serving formats.
+"""Weight construction: HF state dicts / safetensors checkpoints (block-FP8:
+e4m3 with `weight_scale_inv` block scales, fp32 on 128x128 blocks as in
+DeepSeek-V3 or UE8M0 on 32x32 blocks as in the V4 family) and random init
+generated directly in each rank's shard, in the serving formats.
 
 Reference parity: the reference serves weights loaded by SGLang (absent) and
 converts 32x32 ue8m0 block-FP8 to MXFP8 at bind time (dt.py:1-5, fl.py:1-10).
@@ -17,7 +18,7 @@ import torch
 
 from ..config import EngineConfig, ModelConfig
 from ..ops import ExpertWeights
-from ..ops.quant import MXFP8Tensor, mxfp8_from_block128, quant_mxfp8_ref, pack_sf, sf_packed_size, NVFP4Tensor, quant_nvfp4_ref, tile_rows128
+from ..ops.quant import MXFP8Tensor, dequant_blocked, quant_mxfp8_ref, pack_sf, sf_packed_size, NVFP4Tensor, quant_nvfp4_ref, tile_rows128
 from ..parallel.state import ParallelState
 from .deepseek import AttnWeights, DeepseekModel, DenseWeights, LayerWeights, Linear, MoEWeights
 
@@ -122,9 +123,7 @@ def build_model(cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState,
             t = t.to(dev)
             si = si.to(dev) if si is not None else None
         if si is not None:
-            N, K = t.shape
-            s = si.float().repeat_interleave(128, 0)[:N].repeat_interleave(128, 1)[:, :K]
-            t = t.float() * s
+            t = dequant_blocked(t, si)
         return t.float()
 
     def split(t, dim, n, r):
@@ -233,27 +232,48 @@ def load_checkpoint(path: str, names: Optional[Iterable[str]] = None) -> LazyChe
     return LazyCheckpoint(path, names)
 
 
-def save_checkpoint_fp8(sd: Dict[str, torch.Tensor], path: str, cfg: ModelConfig, shard_bytes: int = 1 << 30):
-    """Write a state dict as a DeepSeek-style fp8 checkpoint: every 2-D
-    projection weight as e4m3 + fp32 128x128 `weight_scale_inv`."""
+def _fp8_names(k: str, v: torch.Tensor) -> bool:
+    """The 2-D projection weights a block-FP8 checkpoint stores in e4m3."""
+    if v.dim() != 2:
+        return False
+    return (k.endswith("proj.weight") or ".experts." in k or k.endswith(("wqkv_a.weight", "wq_b.weight",
+                                                                         "wo_b.weight", "wkv.weight")))
+
+
+def save_checkpoint_fp8(sd: Dict[str, torch.Tensor], path: str, cfg: ModelConfig, shard_bytes: int = 1 << 30,
+                        block: int = 128, ue8m0: bool = False):
+    """Write a state dict as a block-FP8 checkpoint: every 2-D projection
+    weight as e4m3 + `weight_scale_inv` per block x block tile (fp32 scales,
+    or UE8M0 powers of two stored as float8_e8m0fnu with ue8m0=True; the V4
+    family's checkpoints use 32 x 32 UE8M0)."""
     from safetensors.torch import save_file
+    from ..ops.quant import ue8m0_ceil_exponent
     os.makedirs(path, exist_ok=True)
     out: Dict[str, torch.Tensor] = {}
     for k, v in sd.items():
-        if v.dim() == 2 and k.endswith("proj.weight") or (".experts." in k and v.dim() == 2):
+        if _fp8_names(k, v):
             N, K = v.shape
-            nb, kb = (N + 127) // 128, (K + 127) // 128
-            pad = torch.zeros(nb * 128, kb * 128)
+            nb, kb = (N + block - 1) // block, (K + block - 1) // block
+            pad = torch.zeros(nb * block, kb * block)
             pad[:N, :K] = v.float()
-            blk = pad.view(nb, 128, kb, 128).abs().amax((1, 3)).clamp(min=1e-12) / 448.0
-            q = (pad.view(nb, 128, kb, 128) / blk.view(nb, 1, kb, 1)).view(nb * 128, kb * 128)[:N, :K]
+            blk = pad.view(nb, block, kb, block).abs().amax((1, 3)).clamp(min=1e-12) / 448.0
+            if ue8m0:
+                e = ue8m0_ceil_exponent(blk)
+                blk = torch.ldexp(torch.ones_like(blk), e)
+            q = (pad.view(nb, block, kb, block) / blk.view(nb, 1, kb, 1)).view(nb * block, kb * block)[:N, :K]
             out[k] = q.to(torch.float8_e4m3fn).contiguous()
-            out[k + "_scale_inv"] = blk.float().contiguous()
+            if ue8m0:
+                out[k + "_scale_inv"] = (e + 127).to(torch.uint8).view(torch.float8_e8m0fnu).contiguous()
+            else:
+                out[k + "_scale_inv"] = blk.float().contiguous()
         else:
             out[k] = v.contiguous()
     save_file(out, os.path.join(path, "model-00001-of-00001.safetensors"))
     d = cfg.to_dict()
-    d["quantization_config"] = {"quant_method": "fp8", "weight_block_size": [128, 128]}
-    d["architectures"] = ["DeepseekV3ForCausalLM"]
+    qc = {"quant_method": "fp8", "weight_block_size": [block, block]}
+    if ue8m0:
+        qc["scale_fmt"] = "ue8m0"
+    d["quantization_config"] = qc
+    d["architectures"] = ["DeepseekV4ForCausalLM" if cfg.is_v4 else "DeepseekV3ForCausalLM"]
     with open(os.path.join(path, "config.json"), "w") as f:
         json.dump(d, f)

@@ -15,8 +15,11 @@ MXFP8 (used for every dense / expert GEMM operand):
 NVFP4 (routed experts in the NVFP4 configuration): e2m1 pairs packed in bytes,
 one e4m3 scale per 16 K elements, one fp32 global scale per tensor.
 
-DeepSeek checkpoints ship e4m3 weights with fp32 128x128 block scales
-(`weight_scale_inv`); :func:`mxfp8_from_block128` converts them at load time.
+Block-FP8 checkpoints ship e4m3 weights with one scale per block of rows x
+columns (`weight_scale_inv`): DeepSeek-V3 uses fp32 scales on 128x128 blocks,
+the V4 family UE8M0 (power-of-two) scales on 32x32 blocks.
+:func:`dequant_blocked` reads either (the block shape follows from the two
+tensors' shapes); the loaders requantize the result to the serving formats.
 """
 from __future__ import annotations
 
@@ -136,13 +139,42 @@ def dequant_mxfp8(q: torch.Tensor, sf: torch.Tensor, packed: bool = True) -> tor
     return (q.float().view(R, K // 32, 32) * scale.unsqueeze(-1)).view(R, K)
 
 
-def mxfp8_from_block128(w: torch.Tensor, scale_inv: torch.Tensor) -> MXFP8Tensor:
-    """Convert a DeepSeek fp8 weight [N, K] with fp32 128x128 block scales
-    [ceil(N/128), ceil(K/128)] to MXFP8 (dequantize, requantize per 32)."""
+def block_scales_float(s: torch.Tensor) -> torch.Tensor:
+    """A checkpoint's block scales as fp32 multipliers: float tensors as they
+    are, UE8M0 bytes (float8_e8m0fnu, or raw uint8) as 2**(byte - 127)."""
+    e8m0 = getattr(torch, "float8_e8m0fnu", None)
+    if s.dtype == torch.uint8 or (e8m0 is not None and s.dtype == e8m0):
+        e = s.view(torch.uint8).to(torch.int32) - 127
+        return torch.ldexp(torch.ones(e.shape, dtype=torch.float32, device=s.device), e)
+    return s.float()
+
+
+def _block_edge(n: int, nb: int) -> int:
+    """The block size along a dimension of n elements cut into nb blocks:
+    the smallest power of two b with ceil(n / b) == nb."""
+    b = 1
+    while (n + b - 1) // b > nb:
+        b *= 2
+    if (n + b - 1) // b != nb:
+        raise ValueError(f"{nb} scale blocks do not tile {n} elements with a power-of-two block")
+    return b
+
+
+def dequant_blocked(w: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    """fp32 [N, K] of a block-FP8 weight: e4m3 w [N, K] times its block
+    scales [ceil(N/bn), ceil(K/bk)] (fp32 or UE8M0; bn x bk = 128 x 128,
+    32 x 32, ... inferred from the shapes)."""
     N, K = w.shape
-    s = scale_inv.float().repeat_interleave(128, 0)[:N].repeat_interleave(128, 1)[:, :K]
-    full = w.float() * s
-    q, sf = quant_mxfp8_ref(full)
+    sn, sk = scale.shape
+    bn, bk = _block_edge(N, sn), _block_edge(K, sk)
+    s = block_scales_float(scale).repeat_interleave(bn, 0)[:N].repeat_interleave(bk, 1)[:, :K]
+    return w.float() * s
+
+
+def mxfp8_from_blocked(w: torch.Tensor, scale: torch.Tensor) -> MXFP8Tensor:
+    """A block-FP8 checkpoint weight [N, K] as MXFP8 (dequantize, then
+    requantize per 32 along K)."""
+    q, sf = quant_mxfp8_ref(dequant_blocked(w, scale))
     return MXFP8Tensor(q, sf)
 
 

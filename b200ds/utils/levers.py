@@ -77,11 +77,13 @@ def add_check(name: str, fn: Callable[[], bool]) -> None:
 
 
 def agree_min(values: List[int], group=None) -> List[int]:
-    """Elementwise MIN over the ranks of `group` (a gloo CPU group)."""
+    """Elementwise MIN over the ranks of `group` (a gloo CPU group); no group
+    (a single-rank parallel state, e.g. a one-GPU model inside a multi-rank
+    job) keeps the values local."""
     import torch
     import torch.distributed as dist
     t = torch.tensor(values, dtype=torch.int64)
-    if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
+    if group is not None and dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MIN, group=group)
     return [int(v) for v in t.tolist()]
 

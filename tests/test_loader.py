@@ -141,3 +141,57 @@ def test_checkpoint_dir_sets_eos(tmp_path):
     (tmp_path / "generation_config.json").write_text(json.dumps({"eos_token_id": [7, 9]}))
     eng = load_engine(str(tmp_path), ecfg=EngineConfig(page_size=8, cuda_graphs=False), device="cpu")
     assert eng.eos == 7
+
+
+def test_dequant_blocked_block_shapes():
+    """Block scales of 128 x 128 (fp32) and 32 x 32 (UE8M0 bytes) with ragged
+    edges: each element is multiplied by its own block's scale."""
+    from b200ds.ops.quant import block_scales_float, dequant_blocked
+    g = torch.Generator().manual_seed(3)
+    for (N, K, b) in ((300, 200, 128), (70, 96, 32), (64, 33, 32)):
+        w = (torch.randn(N, K, generator=g) * 50).to(torch.float8_e4m3fn)
+        nb, kb = (N + b - 1) // b, (K + b - 1) // b
+        if b == 32:
+            e = torch.randint(120, 134, (nb, kb), generator=g).to(torch.uint8)
+            s = e.view(torch.float8_e8m0fnu)
+            sf = torch.pow(2.0, e.float() - 127)
+            assert torch.equal(block_scales_float(s), sf) and torch.equal(block_scales_float(e), sf)
+        else:
+            s = torch.rand(nb, kb, generator=g) + 0.5
+            sf = s
+        want = torch.empty(N, K)
+        for i in range(N):
+            for j in range(K):
+                want[i, j] = w[i, j].float() * sf[i // b, j // b]
+        assert torch.equal(dequant_blocked(w, s), want)
+
+
+def test_v4_ue8m0_block32_checkpoint(tmp_path):
+    """The V4 family's checkpoint format: e4m3 projections with 32 x 32 UE8M0
+    block scales (float8_e8m0fnu `weight_scale_inv`).  The config round-trips
+    and the engine built from the checkpoint generates exactly what a model
+    built from the dequantized weights does."""
+    from b200ds import EngineConfig, SamplingParams, build_model_from
+    from b200ds.config import ModelConfig, tiny_v4_config
+    from b200ds.engine.engine import Engine
+    from b200ds.models.loader import load_checkpoint, save_checkpoint_fp8
+    from b200ds.models.reference_v4 import init_weights_v4
+    from b200ds.ops.quant import dequant_blocked
+    cfg = tiny_v4_config()
+    save_checkpoint_fp8(init_weights_v4(cfg, 0), str(tmp_path), cfg, block=32, ue8m0=True)
+    cfg2 = ModelConfig.from_hf(str(tmp_path / "config.json"))
+    assert cfg2.is_v4 and cfg2.hc_mult == cfg.hc_mult and cfg2.engram_layers == cfg.engram_layers
+    ck = load_checkpoint(str(tmp_path))
+    s = ck["model.layers.0.self_attn.wqkv_a.weight_scale_inv"]
+    assert s.dtype == torch.float8_e8m0fnu
+    w = ck["model.layers.0.self_attn.wqkv_a.weight"]
+    assert w.dtype == torch.float8_e4m3fn and s.shape == ((w.shape[0] + 31) // 32, (w.shape[1] + 31) // 32)
+    deq = {k: (dequant_blocked(v, ck[k + "_scale_inv"]) if k + "_scale_inv" in ck else v)
+           for k, v in ck.items() if not k.endswith("_scale_inv")}
+    prompts = torch.randint(0, cfg.vocab_size, (2, 13), generator=torch.Generator().manual_seed(4)).tolist()
+    outs = []
+    for weights in (str(tmp_path), deq):
+        ecfg = EngineConfig(page_size=8, cuda_graphs=False, enable_prefix_cache=False)
+        eng = Engine(build_model_from(cfg2, ecfg, weights, device="cpu"), ecfg)
+        outs.append([o.token_ids for o in eng.generate(prompts, SamplingParams(max_tokens=5))])
+    assert outs[0] == outs[1]
