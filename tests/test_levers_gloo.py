@@ -19,14 +19,18 @@ def _rank(rank, world):
         return True
     levers.add_check("t_raise", boom)
     res = levers.selfcheck(ps.cpu_group)
-    return res, levers.on("t_good"), levers.on("t_bad"), levers.on("t_raise")
+    # no group: a single-rank parallel state inside the job agrees locally
+    # (only this rank calls it; a collective here would never complete)
+    local = levers.agree_min([10 + rank], None) if rank == 1 else [10]
+    return res, levers.on("t_good"), levers.on("t_bad"), levers.on("t_raise"), local
 
 
 def test_selfcheck_agrees_min_over_ranks():
     out = run_ranks(_rank, 2)
-    for res, good, bad, rz in out:
+    for rank, (res, good, bad, rz, local) in enumerate(out):
         assert res["t_good"] and not res["t_bad"] and not res["t_raise"]
         assert good and not bad and not rz
+        assert local == [10 + rank]
 
 
 def test_switch_env_override(monkeypatch):
