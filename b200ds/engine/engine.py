@@ -269,14 +269,18 @@ class Engine:
         nseq = 0 if step is None else len(step.reqs)
         prefill = step is not None and step.kind == "prefill"
         lp = step is not None and (_wants_lp(step.reqs) or _wants_plp(step))
-        v = torch.tensor([int(prefill), ntok, nseq, int(step is not None), int(lp), int(drafts is not None)],
-                         dtype=torch.int64)
+        decoding = step is not None and not prefill
+        v = torch.tensor([int(prefill), ntok, nseq, int(step is not None), int(lp), int(drafts is not None),
+                          int(decoding)], dtype=torch.int64)
         dist.all_reduce(v, op=dist.ReduceOp.MAX, group=self.ps.cpu_group)
-        any_prefill, max_tok, max_seq, any_work, any_lp, any_verify = (int(x) for x in v)
+        any_prefill, max_tok, max_seq, any_work, any_lp, any_verify, any_decode = (int(x) for x in v)
         if not any_work:
             return None
+        # a rank's decode batch is split between the micro-batches only where
+        # the routing does not depend on the batch (the E5 prune does)
         if (self.ecfg.tbo and any_prefill and not any_lp and not any_verify and self.mtp is None
-                and max_tok >= max(2, self.ecfg.tbo_min_tokens) and getattr(self.model, "supports_tbo", False)):
+                and max_tok >= max(2, self.ecfg.tbo_min_tokens) and getattr(self.model, "supports_tbo", False)
+                and (not any_decode or getattr(self.model, "tbo_splits_decode", True))):
             # every rank splits its rows into two micro-batches the same way
             self.stats["tbo_steps"] = self.stats.get("tbo_steps", 0) + 1
             seqs = [] if step is None else [{"tokens": ch, "start": st, "pages": r.pages}

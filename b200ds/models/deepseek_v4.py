@@ -39,7 +39,7 @@ from ..config import EngineConfig, ModelConfig
 from ..ops import EngramWeights, HcWeights
 from ..parallel.state import ParallelState
 from .batch import ForwardBatch
-from .deepseek import DenseWeights, Linear, MoEWeights
+from .deepseek import DenseWeights, Linear, MoEWeights, _drain
 from .rope import cos_sin_table
 
 
@@ -82,6 +82,14 @@ class _Partial:
 
 class DeepseekV4Model:
     supports_cp = True        # context-parallel prefill under DP attention (parallel/cp.py)
+    supports_tbo = True       # two-batch overlap of DP-attention prefill steps (forward_tbo)
+    _tbo_live = False         # forward_tbo is interleaving micro-batches
+
+    @property
+    def tbo_splits_decode(self) -> bool:
+        """Whether a decode batch may be cut into two micro-batches: not with
+        the E5 prune, whose routing depends on the whole decode batch."""
+        return not self.cfg.prune_budget > 0
 
     def __init__(self, cfg: ModelConfig, ecfg: EngineConfig, ps: ParallelState, layers: List[V4LayerWeights],
                  embed: torch.Tensor, hc_head: HcWeights, final_ln: torch.Tensor, lm_head, device,
@@ -291,20 +299,33 @@ class DeepseekV4Model:
         if fb.is_decode and c.prune_budget > 0:
             w, ids = ops.e5_prune(w, ids, c, c.n_routed_experts)
         if self.dp:
-            return self._moe_dp(mw, h, w, ids, fb)
+            return _drain(self._moe_dp_steps(mw, h, w, ids, fb))
         out = ops.moe_experts(h, w, ids, mw.experts, out_dtype=od, n_experts_total=c.n_routed_experts)
         if mw.shared_gate_up is not None:
             out = out + mw.shared_down(ops.gate_up_swiglu(h, mw.shared_gate_up), out_dtype=od)
         return self._reduce(out.to(od))
 
-    def _moe_dp(self, mw: MoEWeights, h, w: torch.Tensor, ids: torch.Tensor, fb: ForwardBatch) -> torch.Tensor:
+    def _ffn_steps(self, i: int, lw: V4LayerWeights, h, fb: ForwardBatch):
+        """`_ffn` as a generator (yields inside the DP MoE exchange)."""
+        if not (self.dp and isinstance(lw.ffn, MoEWeights)):
+            return self._ffn(i, lw, h, fb)
+        c, mw = self.cfg, lw.ffn
+        w, ids = ops.router(h, mw.gate, mw.bias, c)
+        if fb.is_decode and c.prune_budget > 0:
+            w, ids = ops.e5_prune(w, ids, c, c.n_routed_experts)
+        return (yield from self._moe_dp_steps(mw, h, w, ids, fb))
+
+    def _moe_dp_steps(self, mw: MoEWeights, h, w: torch.Tensor, ids: torch.Tensor, fb: ForwardBatch):
         """Routed experts under DP attention.  Each rank has routed (and, in
         decode, E5-pruned over its own batch) its T_r tokens; tokens, weights
         and expert ids are all-gathered over the EP group, padded to the
         step's agreed T_step rows per rank (padding rows carry no expert),
         every rank runs its local experts over all ranks' rows, the partial
-        sums are all-reduced and each rank keeps its own rows plus its
-        replicated shared expert.  Collectives: NCCL / gloo."""
+        sums are reduce-scattered (all-reduced on gloo) and each rank keeps
+        its own rows plus its replicated shared expert.  A generator that
+        yields right after issuing each collective: asynchronously while two
+        micro-batches interleave (forward_tbo), in place otherwise."""
+        import torch.distributed as dist
         c, ps = self.cfg, self.ps
         od = self._out_dtype()
         T_r = fb.num_tokens
@@ -316,12 +337,31 @@ class DeepseekV4Model:
             x = torch.cat([x, x.new_zeros(pad, x.shape[1])], 0)
             w = torch.cat([w, w.new_zeros(pad, w.shape[1])], 0)
             ids = torch.cat([ids, ids.new_full((pad, ids.shape[1]), -1)], 0)
-        g, gw, gi = ps.ep_all_gather(x.contiguous()), ps.ep_all_gather(w.contiguous()), ps.ep_all_gather(ids.contiguous())
+        overlap = self._tbo_live and not (x.is_cuda and torch.cuda.is_current_stream_capturing())
+        srcs = [x.contiguous(), w.contiguous(), ids.contiguous()]
+        outs = [[torch.empty_like(t) for _ in range(ps.ep_size)] for t in srcs]
+        works = [dist.all_gather(o, t, group=ps.ep_group, async_op=overlap) for o, t in zip(outs, srcs)]
+        yield
+        if overlap:
+            for wk in works:
+                wk.wait()
+        g, gw, gi = (torch.cat(o, 0) for o in outs)
         part = ops.moe_experts(g, gw, gi, mw.experts, out_dtype=torch.float32, n_experts_total=c.n_routed_experts)
-        ps.ep_all_reduce(part)
-        out = part[ps.ep_rank * T_step: ps.ep_rank * T_step + T_r]
+        if dist.get_backend(ps.ep_group) == "nccl":
+            red = torch.empty(T_step, part.shape[1], dtype=part.dtype, device=part.device)
+            work = dist.reduce_scatter_tensor(red, part.contiguous(), group=ps.ep_group, async_op=overlap)
+        else:
+            red = None
+            work = dist.all_reduce(part, group=ps.ep_group, async_op=overlap)
+        shared = None
         if mw.shared_gate_up is not None:
-            out = out + mw.shared_down(ops.gate_up_swiglu(h, mw.shared_gate_up), out_dtype=torch.float32).float()
+            shared = mw.shared_down(ops.gate_up_swiglu(h, mw.shared_gate_up), out_dtype=torch.float32).float()
+        yield
+        if overlap:
+            work.wait()
+        out = red[:T_r] if red is not None else part[ps.ep_rank * T_step: ps.ep_rank * T_step + T_r]
+        if shared is not None:
+            out = out + shared
         return out.to(od)
 
     def _ffn_first_linear(self, lw: V4LayerWeights):
@@ -333,6 +373,36 @@ class DeepseekV4Model:
         """All layers + the head combine; returns (normed hidden, batch) where
         the batch is the prefill tail's when window-only late layers ran on
         a subset of the rows."""
+        return _drain(self._hidden_steps(fb))
+
+    @torch.no_grad()
+    def forward_tbo(self, fbs: List[ForwardBatch]) -> List[torch.Tensor]:
+        """Two-batch overlap (DP attention prefill): the micro-batches' layer
+        stacks run interleaved, each handing over right after it issues a
+        collective of the MoE exchange, so one micro-batch's all-gather /
+        reduce-scatter overlaps the other's kernels; collectives are issued
+        in the same order on every rank.  Returns each micro-batch's logits.
+
+        Reference parity: `_can_run_tbo` / `_forward_layers_tbo` in the V4
+        layer loop (fork_loop.py:121,151-158)."""
+        gens = [self._hidden_steps(fb) for fb in fbs]
+        res = [None] * len(gens)
+        live = list(range(len(gens)))
+        self._tbo_live = True
+        try:
+            while live:
+                for k in list(live):
+                    try:
+                        next(gens[k])
+                    except StopIteration as e:
+                        res[k] = e.value
+                        live.remove(k)
+        finally:
+            self._tbo_live = False
+        return [ops.lm_head_logits(self._last_hidden(h, fb), self.lm_head, self.ps) for h, fb in res]
+
+    def _hidden_steps(self, fb: ForwardBatch):
+        """`_hidden` as a generator: yields inside the DP MoE exchanges."""
         c = self.cfg
         eps = c.rms_norm_eps
         tr = self.tracer
@@ -381,7 +451,8 @@ class DeepseekV4Model:
             moe = isinstance(lw.ffn, MoEWeights)
             h, post, comb = ops.hc_boundary(X, carry, lw.ffn_hc, lw.post_ln, eps, c, self._ffn_first_linear(lw),
                                             keep_hf=moe, sumsq=ss)
-            carry, ss = (self._ffn(i, lw, h, fb), post, comb), None
+            f = yield from self._ffn_steps(i, lw, h, fb)
+            carry, ss = (f, post, comb), None
         tr.mark("head")
         if isinstance(carry[0], _Partial):
             ss = self._post(X, *carry)

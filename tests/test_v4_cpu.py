@@ -1,6 +1,7 @@
 """DeepSeek-V4 family on CPU: mHC coefficient properties, the E5 prune rule,
 Engram hashing through the per-slot token cache, the engine's V4 model
 against the fp32 oracle (greedy tokens, logits), and TP=2 over gloo."""
+import pytest
 import torch
 
 from mp_util import run_ranks
@@ -254,3 +255,71 @@ def test_v4_window_late_layers_prefill_tail_matches_oracle():
     assert toks == want and skipped == 0
     toks, skipped = run(enable_prefix_cache=True)
     assert toks == want and skipped == 0
+
+
+def _v4_tbo_cfg(compressed):
+    from b200ds.config import tiny_v4_config
+    if compressed:
+        return tiny_v4_config(index_n_heads=8, index_head_dim=32, index_topk=6, index_swa=4,
+                              compress_ratios=(0, 2, 4), compress_topk=4)
+    return tiny_v4_config()
+
+
+def _tbo_rank(rank, world, compressed):
+    from b200ds import build_model_from
+    from b200ds.config import EngineConfig
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.reference_v4 import init_weights_v4
+    from b200ds.parallel.state import init_parallel
+    ps = init_parallel(backend="gloo", dp_attention=True)
+    cfg = _v4_tbo_cfg(compressed)
+    ecfg = EngineConfig(page_size=8, cuda_graphs=False, enable_prefix_cache=False, max_prefill_tokens=9,
+                        tp_size=1, ep_size=world, dp_attention=True, tbo=True, tbo_min_tokens=4)
+    eng = Engine(build_model_from(cfg, ecfg, init_weights_v4(cfg, 0), device="cpu", ps=ps), ecfg)
+    mine = [i for i in range(4) if i % world == rank]
+    prompts = _tbo_prompts(cfg)
+    split_decode = []
+    orig = eng._tbo_logits
+
+    def spy(seqs, max_tok):
+        split_decode.append(bool(seqs) and all(len(q["tokens"]) == 1 for q in seqs) and len(seqs) > 1)
+        return orig(seqs, max_tok)
+    eng._tbo_logits = spy
+    outs = eng.generate([prompts[i] for i in mine], [SamplingParams(max_tokens=TBO_MAXT[i]) for i in mine])
+    return mine, [o.token_ids for o in outs], eng.stats.get("tbo_steps", 0), any(split_decode)
+
+
+TBO_MAXT = [6, 8, 3, 8]
+
+
+def _tbo_prompts(cfg):
+    # rank 0: a 30-token prompt still prefilling while rank 1's two short
+    # prompts already decode (a two-row decode batch inside overlapped steps)
+    g = torch.Generator().manual_seed(8)
+    return [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (30, 5, 4, 5)]
+
+
+@pytest.mark.parametrize("compressed", [False, True])
+def test_v4_dp2_two_batch_overlap_gloo(compressed):
+    """Two-batch overlap for the V4 family under DP attention: prefill rows
+    split in two micro-batches whose layer stacks interleave at the MoE
+    exchange (Engram hashes, mHC and, compressed, the block compressor across
+    the cut); steps where a rank decodes keep its batch whole (the E5 prune
+    routes over the whole decode batch).  Tokens equal a single-process run."""
+    from b200ds import build_model_from
+    from b200ds.config import EngineConfig
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.reference_v4 import init_weights_v4
+    cfg = _v4_tbo_cfg(compressed)
+    res = run_ranks(_tbo_rank, 2, compressed)
+    assert sum(r[2] for r in res) >= 1
+    assert not any(r[3] for r in res)        # no multi-row decode batch went through the split
+    prompts = _tbo_prompts(cfg)
+    for mine, toks, _, _ in res:
+        ecfg = EngineConfig(page_size=8, cuda_graphs=False, enable_prefix_cache=False, max_prefill_tokens=9)
+        eng = Engine(build_model_from(cfg, ecfg, init_weights_v4(cfg, 0), device="cpu"), ecfg)
+        want = [o.token_ids for o in eng.generate([prompts[i] for i in mine],
+                                                  [SamplingParams(max_tokens=TBO_MAXT[i]) for i in mine])]
+        assert toks == want, (mine, toks, want)
