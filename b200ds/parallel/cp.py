@@ -86,20 +86,18 @@ class CPLayout:
 
 def layout(start: int, n: int, world: int, pages: Sequence[int], page_size: int,
            tokens: Sequence[int] = ()) -> CPLayout:
+    """Chunk position start + k sits on rank k % W as that rank's row k // W,
+    so in position order the gathered rows are (k % W) * tmax + k // W."""
     counts = [len(range(q, n, world)) for q in range(world)]
     tmax = max(max(counts), 1)
-    src, pos = [], []
-    for q in range(world):
-        for j in range(counts[q]):
-            src.append(q * tmax + j)
-            pos.append(start + q + j * world)
-    order = sorted(range(n), key=lambda k: pos[k])
-    src = [src[k] for k in order]
-    pos = [pos[k] for k in order]
-    slots = [pages[p // page_size] * page_size + p % page_size for p in pos]
-    ids = [tokens[p] for p in pos] if tokens else [0] * n
-    return CPLayout(counts, tmax, start, torch.tensor(src, dtype=torch.int64), torch.tensor(slots, dtype=torch.int64),
-                    torch.tensor(ids, dtype=torch.int32))
+    k = torch.arange(n, dtype=torch.int64)
+    src = (k % world) * tmax + k // world
+    pos = start + k
+    pg = torch.as_tensor(list(pages), dtype=torch.int64)
+    slots = pg[pos // page_size] * page_size + pos % page_size
+    ids = (torch.as_tensor(list(tokens[start:start + n]), dtype=torch.int32) if len(tokens)
+           else torch.zeros(n, dtype=torch.int32))
+    return CPLayout(counts, tmax, start, src, slots, ids)
 
 
 def build_cp_batch(prompt: Sequence[int], start: int, n: int, world: int, rank: int, pages: Sequence[int],
