@@ -847,13 +847,18 @@ class Engine:
             _cuda.check_device_errors()
 
     def generate(self, prompts: Sequence[Union[str, Sequence[int]]],
-                 params: Union[SamplingParams, Sequence[SamplingParams], None] = None) -> List[GenerateOutput]:
+                 params: Union[SamplingParams, Sequence[SamplingParams], None] = None,
+                 cp_owner: Union[int, Sequence[Optional[int]], None] = None) -> List[GenerateOutput]:
         """Run the prompts to completion and return one output per prompt
         (in order).  Identical calls on every rank of an SPMD job produce
-        identical results."""
+        identical results.  cp_owner (context_parallel engines; one rank for
+        all prompts or one per prompt, None = ordinary): the prompts prefill
+        on every rank and decode on their owner, so every rank passes the
+        same prompts; the other ranks' outputs are empty."""
         if params is None or isinstance(params, SamplingParams):
             params = [params or SamplingParams()] * len(prompts)
-        reqs = [self.add_request(p, sp) for p, sp in zip(prompts, params)]
+        owners = cp_owner if isinstance(cp_owner, (list, tuple)) else [cp_owner] * len(prompts)
+        reqs = [self.add_request(p, sp, cp_owner=o) for p, sp, o in zip(prompts, params, owners)]
         while any(not r.finished for r in reqs):
             self.step()
         self._drain_dp()

@@ -188,3 +188,29 @@ def test_cp2_v4_prefill_matches_single(compressed):
             assert out == want and reason == "length"
         else:
             assert out == [] and reason == "context_parallel_peer"
+
+
+def _rank_generate(rank, world):
+    from b200ds import build_model_from
+    from b200ds.config import EngineConfig
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.reference import init_weights
+    from b200ds.parallel.state import init_parallel
+    ps = init_parallel(backend="gloo", dp_attention=True)
+    cfg = _cfg(False)
+    ecfg = EngineConfig(page_size=8, cuda_graphs=False, tp_size=1, ep_size=world, dp_attention=True,
+                        context_parallel=True, max_prefill_tokens=8)
+    eng = Engine(build_model_from(cfg, ecfg, init_weights(cfg, 0), device="cpu", ps=ps), ecfg)
+    prompts = _prompts(cfg)
+    outs = eng.generate(prompts[:2], SamplingParams(max_tokens=5), cp_owner=[0, 1])
+    return rank, [o.token_ids for o in outs]
+
+
+def test_cp2_generate_with_owners():
+    """Engine.generate with per-prompt owners: both prompts prefill on both
+    ranks, prompt i decodes on rank i."""
+    cfg = _cfg(False)
+    ref = _single(cfg, _prompts(cfg)[:2], [5, 5])
+    for rank, toks in run_ranks(_rank_generate, 2):
+        assert toks[rank] == ref[rank] and toks[1 - rank] == []
