@@ -320,12 +320,24 @@ class DeepseekModel:
         T_step = max(int(fb.dp_tmax or 0), T_r)
         out_dt = torch.float32 if self.device.type == "cpu" else torch.bfloat16
         x = ops.to_float(h)
-        if T_step > T_r:
-            x = torch.cat([x, x.new_zeros(T_step - T_r, x.shape[1])], 0)
-        x = x.to(out_dt).contiguous()
         # asynchronous only while two micro-batches interleave (never inside a
         # graph capture); otherwise the collectives complete in place
         overlap = self._tbo_live and not (x.is_cuda and torch.cuda.is_current_stream_capturing())
+        from ..parallel.ep_a2a import a2a_moe_steps, a2a_ok
+        if a2a_ok(x, T_step):
+            # rows travel only to their experts' owners (router on the local rows)
+            w, ids = ops.router(h, mw.gate, mw.bias, c)
+
+            def run(xr, wr, ir):
+                return ops.moe_experts(xr, wr, ir, mw.experts, out_dtype=torch.float32,
+                                       n_experts_total=c.n_routed_experts)
+            out = yield from a2a_moe_steps(x.to(out_dt).contiguous(), w, ids, ps, mw.experts.count, run, overlap)
+            if mw.shared_gate_up is not None:
+                out = out + mw.shared_down(ops.gate_up_swiglu(h, mw.shared_gate_up), out_dtype=torch.float32).float()
+            return out.to(out_dt)
+        if T_step > T_r:
+            x = torch.cat([x, x.new_zeros(T_step - T_r, x.shape[1])], 0)
+        x = x.to(out_dt).contiguous()
         parts = [torch.empty_like(x) for _ in range(ps.ep_size)]
         work = dist.all_gather(parts, x, group=ps.ep_group, async_op=overlap)
         yield

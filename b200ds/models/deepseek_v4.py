@@ -332,6 +332,18 @@ class DeepseekV4Model:
         T_step = max(int(fb.dp_tmax or 0), T_r)
         x = ops.to_float(h).to(od)
         w = w.float()
+        from ..parallel.ep_a2a import a2a_moe_steps, a2a_ok
+        if a2a_ok(x, T_step):
+            # rows travel only to their experts' owners
+            overlap = self._tbo_live and not (x.is_cuda and torch.cuda.is_current_stream_capturing())
+
+            def run(xr, wr, ir):
+                return ops.moe_experts(xr, wr, ir, mw.experts, out_dtype=torch.float32,
+                                       n_experts_total=c.n_routed_experts)
+            out = yield from a2a_moe_steps(x.contiguous(), w, ids, ps, mw.experts.count, run, overlap)
+            if mw.shared_gate_up is not None:
+                out = out + mw.shared_down(ops.gate_up_swiglu(h, mw.shared_gate_up), out_dtype=torch.float32).float()
+            return out.to(od)
         if T_step > T_r:
             pad = T_step - T_r
             x = torch.cat([x, x.new_zeros(pad, x.shape[1])], 0)

@@ -126,6 +126,10 @@ register("nvls", "B200_NVLS", True,
          "tensor-parallel all-reduces through NVLink multicast (multimem.ld_reduce / multimem.st in the switch) on "
          "groups of B200_NVLS_MIN_WORLD or more ranks with multicast support (default 16: off on one 8-GPU "
          "box, where it measured slower than the push protocol and NCCL)")
+register("dp_moe_a2a", "B200_DP_MOE_A2A", True,
+         "DP-attention steps too large for the fused dispatch buffers exchange MoE rows all-to-all (each row to its "
+         "experts' owners only) instead of all-gather + reduce-scatter; rows per rank >= B200_DP_A2A_MIN_ROWS "
+         "(default 64), never inside a graph capture")
 register("l2_prefetch", "B200_L2_PREFETCH", True,
          "decode layers pull the o-projection (and shared-expert) weights into L2 on a low-priority side stream "
          "while attention runs")

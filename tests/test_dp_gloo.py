@@ -133,3 +133,54 @@ def test_dp2_two_batch_overlap_matches_single(idle_rank1):
     for mine, toks, tbo_steps in res:
         assert tbo_steps >= 1
         assert toks == [ref[i] for i in mine]
+
+
+def _a2a_rank(rank, world, tbo):
+    import os
+    os.environ["B200_DP_A2A_MIN_ROWS"] = "1"        # every step takes the all-to-all exchange
+    from b200ds import build_model_from
+    from b200ds.config import EngineConfig, tiny_config
+    from b200ds.engine.engine import Engine
+    from b200ds.engine.request import SamplingParams
+    from b200ds.models.reference import init_weights
+    from b200ds.parallel import ep_a2a
+    from b200ds.parallel.state import init_parallel
+    calls = []
+    orig = ep_a2a.a2a_moe_steps
+
+    def spy(*a, **k):
+        calls.append(1)
+        return (yield from orig(*a, **k))
+    ep_a2a.a2a_moe_steps = spy
+    ps = init_parallel(backend="gloo", dp_attention=True)
+    cfg = tiny_config()
+    ecfg = EngineConfig(page_size=8, cuda_graphs=False, tp_size=1, ep_size=world, dp_attention=True,
+                        tbo=tbo, tbo_min_tokens=4)
+    eng = Engine(build_model_from(cfg, ecfg, init_weights(cfg, 0), device="cpu", ps=ps), ecfg)
+    mine = [i for i in range(3) if i % world == rank]
+    outs = eng.generate([_prompts(cfg)[i] for i in mine], [SamplingParams(max_tokens=_max_tokens()[i]) for i in mine])
+    return mine, [o.token_ids for o in outs], len(calls)
+
+
+@pytest.mark.parametrize("tbo", [False, True])
+def test_dp2_all_to_all_exchange_matches_single(tbo):
+    """The all-to-all MoE exchange (each row only to its experts' owners,
+    partial sums back to the source rows), alone and interleaved by two-batch
+    overlap: tokens equal a single-process run."""
+    from b200ds.config import EngineConfig, tiny_config
+    cfg = tiny_config()
+    ref, _ = _run(cfg, EngineConfig(page_size=8, cuda_graphs=False), _prompts(cfg), _max_tokens())
+    res = run_ranks(_a2a_rank, 2, tbo)
+    for mine, toks, calls in res:
+        assert calls > 0
+        assert toks == [ref[i] for i in mine]
+
+
+def test_a2a_send_plan():
+    """Rows go once to every rank owning one of their experts."""
+    import torch
+    from b200ds.parallel.ep_a2a import send_plan
+    ids = torch.tensor([[0, 5], [1, 2], [7, -1], [6, 4]])     # 8 experts, 2 per rank, 4 ranks
+    row, counts = send_plan(ids, 2, 4)
+    assert counts.tolist() == [2, 1, 2, 2]
+    assert row.tolist() == [0, 1, 1, 0, 3, 2, 3]

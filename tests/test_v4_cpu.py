@@ -323,3 +323,24 @@ def test_v4_dp2_two_batch_overlap_gloo(compressed):
         want = [o.token_ids for o in eng.generate([prompts[i] for i in mine],
                                                   [SamplingParams(max_tokens=TBO_MAXT[i]) for i in mine])]
         assert toks == want, (mine, toks, want)
+
+
+def _dp_rank_a2a(rank, world):
+    import os
+    os.environ["B200_DP_A2A_MIN_ROWS"] = "1"        # every step takes the all-to-all exchange
+    return _dp_rank(rank, world)
+
+
+def test_v4_dp2_all_to_all_exchange_gloo():
+    """The V4 family's DP MoE through the all-to-all exchange (rows only to
+    their experts' owners; E5-pruned decode routing travels with the rows):
+    each rank's tokens equal a single-process run of its own requests."""
+    from b200ds.engine.request import SamplingParams
+    res = run_ranks(_dp_rank_a2a, 2)
+    for mine, toks in res:
+        eng, cfg = _v4_engine(chunk=7)
+        prompts = _prompts(cfg, 3, 11, seed=6)
+        maxt = [7, 4, 9]
+        want = [o.token_ids for o in eng.generate([prompts[i].tolist() for i in mine],
+                                                  [SamplingParams(max_tokens=maxt[i]) for i in mine])]
+        assert toks == want, (mine, toks, want)
