@@ -155,6 +155,9 @@ def _dp_rank(rank, world, comm_impl, fmt="mxfp8"):
     if comm_impl == "peer":       # the expert kernels read the routed rows from their source ranks over NVLink
         levers.set_switch("ep_peer_pull", True)
         comm_impl = "fused"
+    if comm_impl == "a2a":        # NCCL all-to-all exchange: rows only to their experts' owners
+        os.environ["B200_DP_A2A_MIN_ROWS"] = "1"
+        comm_impl = "nccl"
     ps = init_parallel(backend="nccl", dp_attention=True, timeout_s=60)
     ops.set_impl("native")
     cfg = small_gpu_config(num_attention_heads=16, expert_format=fmt)
@@ -176,7 +179,7 @@ def _dp_rank(rank, world, comm_impl, fmt="mxfp8"):
 
 
 @pytest.mark.parametrize("comm_impl,fmt", [("nccl", "mxfp8"), ("fused", "mxfp8"), ("fused", "nvfp4"),
-                                           ("peer", "mxfp8"), ("peer", "nvfp4")])
+                                           ("peer", "mxfp8"), ("peer", "nvfp4"), ("a2a", "mxfp8")])
 def test_dp2_ep2_matches_single_gpu(comm_impl, fmt):
     """DP attention + EP MoE on 2 GPUs, ranks with different token counts:
     each rank's logits follow a 1-GPU run of its own batch (fp8 noise only).
