@@ -1,5 +1,5 @@
 """Engine features that ride on the GPU kernels, run on a B200: loading an HF
-fp8 checkpoint (128 x 128 block scales) with the dequantize / requantize on
+fp8 checkpoint (128 x 128 fp32 or 32 x 32 UE8M0 block scales) with the dequantize / requantize on
 the device, the full-logits step path (log-probabilities, penalties, guided
 decoding) next to the decode graphs, the host-memory tier of the prefix
 cache, and the tactic tuner."""
@@ -30,10 +30,12 @@ def _rel(a, b):
     return ((a.float() - b.float()).norm() / b.float().norm()).item()
 
 
-def test_fp8_checkpoint_loads_on_the_gpu(tmp_path):
+@pytest.mark.parametrize("block,ue8m0", [(128, False), (32, True)])
+def test_fp8_checkpoint_loads_on_the_gpu(tmp_path, block, ue8m0):
     """Checkpoint bytes cross the host link as fp8 and are dequantized
-    (128 x 128 scales) and requantized to the serving formats on the device;
-    the served model follows the one built straight from the same weights."""
+    (128 x 128 fp32 or 32 x 32 UE8M0 block scales) and requantized to the
+    serving formats on the device; the served model follows the one built
+    straight from the same weights."""
     from b200ds import EngineConfig, SamplingParams, build_model_from, load_engine
     from b200ds.config import small_gpu_config
     from b200ds.engine.engine import Engine
@@ -42,7 +44,7 @@ def test_fp8_checkpoint_loads_on_the_gpu(tmp_path):
     from b200ds.ops.quant import dequant_mxfp8
     cfg = small_gpu_config(num_hidden_layers=2)
     sd = init_weights(cfg, 0)
-    save_checkpoint_fp8(sd, str(tmp_path), cfg)
+    save_checkpoint_fp8(sd, str(tmp_path), cfg, block=block, ue8m0=ue8m0)
     ecfg = EngineConfig(page_size=64, max_kv_pages=64, cuda_graphs=False)
     eng = load_engine(cfg, weights=str(tmp_path), ecfg=ecfg, device="cuda")
     w = eng.model.layers[0].attn.o_proj.w
@@ -50,8 +52,8 @@ def test_fp8_checkpoint_loads_on_the_gpu(tmp_path):
     from b200ds.models.loader import load_checkpoint
     ck = load_checkpoint(str(tmp_path))
     k = "model.layers.0.self_attn.o_proj.weight"
-    v, s = ck[k].float(), ck[k + "_scale_inv"].float()
-    deq = v * s.repeat_interleave(128, 0)[: v.shape[0]].repeat_interleave(128, 1)[:, : v.shape[1]]
+    from b200ds.ops.quant import dequant_blocked
+    deq = dequant_blocked(ck[k], ck[k + "_scale_inv"])
     srv = dequant_mxfp8(w.data.cpu(), w.sf.cpu())[: cfg.hidden_size]
     assert _rel(srv, deq) < 0.03
     direct = Engine(build_model_from(cfg, ecfg, sd, device="cuda"), ecfg)
