@@ -1,6 +1,7 @@
 """Property tests (hypothesis) of the format and routing references the
 kernels are checked against: scale-layout packing, tiling, MXFP8 / NVFP4
-error bounds, Sinkhorn, E5 prune invariants, Engram hash ranges."""
+error bounds, Sinkhorn, E5 prune invariants, Engram hash ranges, the context-parallel
+row layout and the all-to-all send plan."""
 import torch
 from hypothesis import given, settings
 from hypothesis import strategies as st
@@ -89,3 +90,49 @@ def test_engram_hash_head_ranges(T, heads, n, seed):
     j = torch.arange(heads).unsqueeze(0)
     assert bool(((out >= j * per) & (out < (j + 1) * per)).all())
     assert torch.equal(out, ref.engram_hash(ctx, heads, rows, n))
+
+
+@settings(max_examples=40, deadline=None)
+@given(st.integers(0, 200), st.integers(1, 300), st.integers(1, 8), st.sampled_from([8, 16, 64]),
+       st.integers(0, 2 ** 31 - 1))
+def test_cp_layout_covers_the_chunk(start, n, world, page, seed):
+    """Context-parallel layout: every chunk position is computed by exactly
+    one rank, gathered rows land on that position's slot, and each rank's
+    batch holds its strided rows (or one dummy row on the scratch page)."""
+    import random
+    from b200ds.parallel.cp import build_cp_batch, layout
+    rnd = random.Random(seed)
+    npages = (start + n + page - 1) // page
+    pages = rnd.sample(range(1, 4 * npages + 2), npages)
+    prompt = [rnd.randrange(1000) for _ in range(start + n)]
+    lay = layout(start, n, world, pages, page, prompt)
+    assert sum(lay.counts) == n and lay.tmax == max(max(lay.counts), 1)
+    gathered = {}
+    for q in range(world):
+        fb = build_cp_batch(prompt, start, n, world, q, pages, page)
+        if lay.counts[q] == 0:
+            assert fb.out_slots.tolist() == [0]
+            continue
+        assert fb.positions.tolist() == list(range(start + q, start + n, world))
+        for j, (p, slot) in enumerate(zip(fb.positions.tolist(), fb.out_slots.tolist())):
+            gathered[q * lay.tmax + j] = (p, slot, fb.input_ids[j].item())
+    for k in range(n):
+        p, slot, tok = gathered[int(lay.src_rows[k])]
+        assert p == start + k and slot == int(lay.dst_slots[k]) and tok == int(lay.ids[k]) == prompt[p]
+
+
+@settings(max_examples=40, deadline=None)
+@given(st.integers(1, 60), st.integers(1, 8), st.sampled_from([1, 2, 4, 8]), st.integers(1, 4),
+       st.integers(0, 2 ** 31 - 1))
+def test_a2a_send_plan_properties(T, K, world, e_local, seed):
+    """All-to-all send plan: row t goes to rank d exactly when one of its
+    experts lives there, once, in destination-then-row order."""
+    from b200ds.parallel.ep_a2a import send_plan
+    g = torch.Generator().manual_seed(seed)
+    E = world * e_local
+    ids = torch.randint(-1, E, (T, K), generator=g)
+    row, counts = send_plan(ids, e_local, world)
+    want = [sorted({t for t in range(T) for e in ids[t].tolist() if e >= 0 and e // e_local == d})
+            for d in range(world)]
+    assert counts.tolist() == [len(w) for w in want]
+    assert row.tolist() == [t for w in want for t in w]
