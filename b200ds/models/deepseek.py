@@ -309,11 +309,13 @@ class DeepseekModel:
 
     def _moe_dp_host(self, mw: MoEWeights, h, fb: ForwardBatch):
         """Host-collective MoE under DP attention, as a generator that yields
-        right after issuing each collective (asynchronously), so two-batch
-        overlap can run the other micro-batch's work meanwhile: all-gather of
-        every rank's rows, this rank's experts over all of them, then a
-        reduce-scatter (NCCL; all-reduce + own slice on gloo) back to the
-        owners; the shared expert runs during the reduction."""
+        right after issuing each collective (asynchronously while two-batch
+        overlap interleaves micro-batches).  Large steps: the all-to-all
+        exchange (parallel/ep_a2a.py: rows only to their experts' owners,
+        partial sums back).  Smaller ones: all-gather of every rank's rows,
+        this rank's experts over all of them, then a reduce-scatter (NCCL;
+        all-reduce + own slice on gloo) back to the owners.  The shared
+        expert runs during the reduction."""
         import torch.distributed as dist
         c, ps = self.cfg, self.ps
         T_r = fb.num_tokens
