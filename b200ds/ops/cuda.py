@@ -6,7 +6,8 @@ extension raises: there is no silent fallback.
 from __future__ import annotations
 
 import os
-from typing import Optional
+import weakref
+from typing import List, Optional
 
 import torch
 import torch.distributed as dist
@@ -391,19 +392,25 @@ def _moe_ws(ex, dev) -> torch.Tensor:
         ws = torch.zeros(2 + ex.count, dtype=torch.int32, device=dev)
         ex._fused_ws = ws
         ex._fused_err = torch.zeros(1, dtype=torch.int32, device=dev)
-        _ERR_WORDS.append(ex._fused_err)
+        _ERR_WORDS.append(weakref.ref(ex._fused_err))
     return ws
 
 
-_ERR_WORDS = []     # device error words of kernels with in-kernel waits
+# device error words of kernels with in-kernel waits (weak: a word lives as
+# long as its expert set)
+_ERR_WORDS: List[weakref.ref] = []
 
 
 def check_device_errors() -> None:
     """Raise if a bounded in-kernel wait (dependency between CTAs) ran out.
-    One device read for all error words (one per expert set)."""
-    if not _ERR_WORDS:
+    One device read for all live error words (one per expert set)."""
+    words = [w() for w in _ERR_WORDS]
+    words = [w for w in words if w is not None]
+    if len(words) != len(_ERR_WORDS):
+        _ERR_WORDS[:] = [weakref.ref(w) for w in words]
+    if not words:
         return
-    v = int(torch.cat(_ERR_WORDS).max().item()) if len(_ERR_WORDS) > 1 else int(_ERR_WORDS[0].item())
+    v = int(torch.cat(words).max().item()) if len(words) > 1 else int(words[0].item())
     if v:
         raise RuntimeError(f"fused expert GEMM: in-kernel dependency wait timed out (code {v})")
 
