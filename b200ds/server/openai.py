@@ -443,11 +443,11 @@ class _Metrics:
             f'b200ds_step_seconds{{quantile="0.5"}} {q(self.step_time[-1000:], 0.5)}',
         ]
         st = engine_stats or {}
-        for k in ("steps", "prefill_tokens", "decode_tokens", "spec_proposed", "spec_accepted"):
+        for k in ("steps", "prefill_tokens", "decode_tokens", "spec_proposed", "spec_accepted", "tbo_steps"):
             if k in st:
                 lines.append(f"b200ds_engine_{k}_total {int(st[k])}")
         g = gauges or {}
-        for k in ("running", "prefilling", "waiting", "kv_pages_total", "kv_pages_free"):
+        for k in ("running", "prefilling", "waiting", "kv_pages_total", "kv_pages_free", "cp_queue"):
             if k in g:
                 lines.append(f"b200ds_{k} {int(g[k])}")
         for k in ("admitted_prompt_tokens", "prefix_hit_tokens", "preemptions", "host_offloads", "host_restores"):

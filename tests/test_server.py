@@ -49,6 +49,7 @@ def test_chat_and_models_and_metrics(client):
     assert "b200ds_requests_completed_total" in m
     assert "b200ds_engine_decode_tokens_total" in m and 'b200ds_switch{name="moe_fused"}' in m
     assert "b200ds_kv_pages_free" in m and "b200ds_prefix_cache_hit_ratio" in m and "b200ds_preemptions_total" in m
+    assert "b200ds_cp_queue 0" in m
 
 
 def test_stop_strings(client):
