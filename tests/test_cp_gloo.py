@@ -43,7 +43,10 @@ def _single(cfg, prompts, maxt):
     return [o.token_ids for o in outs]
 
 
-def _rank(rank, world, sparse, owner):
+def _rank(rank, world, sparse, owner, a2a=False):
+    if a2a:
+        import os
+        os.environ["B200_DP_A2A_MIN_ROWS"] = "1"    # the chunks' MoE rows go all-to-all
     from b200ds import build_model_from
     from b200ds.config import EngineConfig
     from b200ds.engine.engine import Engine
@@ -64,13 +67,13 @@ def _rank(rank, world, sparse, owner):
     return rank, own.output, cp.output, cp.finish_reason, eng.pool.num_free, eng.stats["prefill_tokens"]
 
 
-@pytest.mark.parametrize("sparse", [False, True])
-def test_cp2_prefill_matches_single(sparse):
+@pytest.mark.parametrize("sparse,a2a", [(False, False), (True, False), (False, True)])
+def test_cp2_prefill_matches_single(sparse, a2a):
     cfg = _cfg(sparse)
     prompts = _prompts(cfg)
     ref = _single(cfg, prompts, MAXT)
     owner = 1       # the prompt's last row is computed on rank 0: the row crosses ranks
-    res = run_ranks(_rank, 2, sparse, owner)
+    res = run_ranks(_rank, 2, sparse, owner, a2a)
     for rank, own, cp, reason, _, _ in res:
         assert own == ref[1 + rank]
         if rank == owner:
